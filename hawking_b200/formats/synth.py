@@ -1,0 +1,94 @@
+"""Seeded synthetic model writers (random-init weights of a named architecture).
+
+The engine is benchmarked on random-init weights; these writers produce byte-faithful GGUF
+files for the llama family (llama / qwen2 / mixtral / qwen3moe) so every loader path is the
+same one a real checkpoint takes. Weights are N(0, std) from ``seed``; RMSNorm weights are 1.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from ..models.config import ModelConfig
+from .ggml import GgmlType, type_id
+from .gguf import GgufBuilder
+
+
+def _gguf_arch(cfg: ModelConfig) -> str:
+    return "llama" if cfg.arch in ("llama", "mixtral") else cfg.arch
+
+
+def write_llama_family_gguf(path: str, cfg: ModelConfig, seed: int = 0, std: float = 0.02,
+                            threads: int = 8) -> str:
+    arch = _gguf_arch(cfg)
+    rng = np.random.default_rng(seed)
+    wt = type_id(cfg.weight_type)
+    et = type_id(cfg.embed_type or cfg.weight_type)
+    b = GgufBuilder(arch)
+    b.set("general.name", f"synthetic-{cfg.arch}")
+    b.arch_set("vocab_size", cfg.vocab)
+    b.arch_set("context_length", cfg.max_ctx)
+    b.arch_set("embedding_length", cfg.hidden)
+    b.arch_set("block_count", cfg.layers)
+    b.arch_set("feed_forward_length", cfg.ffn)
+    b.arch_set("attention.head_count", cfg.n_heads)
+    b.arch_set("attention.head_count_kv", cfg.n_kv_heads)
+    b.arch_set("rope.dimension_count", cfg.rope_dim)
+    b.set_f32(f"{arch}.rope.freq_base", cfg.rope_theta)
+    b.set_f32(f"{arch}.attention.layer_norm_rms_epsilon", cfg.eps)
+    if cfg.head_dim * cfg.n_heads != cfg.hidden:
+        b.arch_set("attention.key_length", cfg.head_dim)
+        b.arch_set("attention.value_length", cfg.head_dim)
+    if cfg.is_moe:
+        b.arch_set("expert_count", cfg.n_experts)
+        b.arch_set("expert_used_count", cfg.top_k)
+        if cfg.expert_ffn != cfg.ffn:
+            b.arch_set("expert_feed_forward_length", cfg.expert_ffn)
+        if cfg.shared_ffn:
+            b.arch_set("expert_shared_feed_forward_length", cfg.shared_ffn)
+
+    def w(*shape):
+        return (rng.standard_normal(shape, dtype=np.float32) * std).astype(np.float32)
+
+    H, hd, F = cfg.hidden, cfg.head_dim, cfg.ffn
+    b.add("token_embd.weight", w(cfg.vocab, H), et, threads)
+    for l in range(cfg.layers):
+        p = f"blk.{l}."
+        b.add(p + "attn_norm.weight", np.ones(H, np.float32), GgmlType.F32)
+        b.add(p + "attn_q.weight", w(cfg.n_heads * hd, H), wt, threads)
+        b.add(p + "attn_k.weight", w(cfg.n_kv_heads * hd, H), wt, threads)
+        b.add(p + "attn_v.weight", w(cfg.n_kv_heads * hd, H), wt, threads)
+        if cfg.qkv_bias:
+            b.add(p + "attn_q.bias", w(cfg.n_heads * hd), GgmlType.F32)
+            b.add(p + "attn_k.bias", w(cfg.n_kv_heads * hd), GgmlType.F32)
+            b.add(p + "attn_v.bias", w(cfg.n_kv_heads * hd), GgmlType.F32)
+        if cfg.qk_norm:
+            b.add(p + "attn_q_norm.weight", np.ones(hd, np.float32), GgmlType.F32)
+            b.add(p + "attn_k_norm.weight", np.ones(hd, np.float32), GgmlType.F32)
+        b.add(p + "attn_output.weight", w(H, cfg.n_heads * hd), wt, threads)
+        b.add(p + "ffn_norm.weight", np.ones(H, np.float32), GgmlType.F32)
+        if cfg.is_moe:
+            E, Fe = cfg.n_experts, cfg.expert_ffn
+            b.add(p + "ffn_gate_inp.weight", w(E, H), GgmlType.F32)
+            b.add(p + "ffn_gate_exps.weight", w(E, Fe, H), wt, threads)
+            b.add(p + "ffn_up_exps.weight", w(E, Fe, H), wt, threads)
+            b.add(p + "ffn_down_exps.weight", w(E, H, Fe), wt, threads)
+            if cfg.shared_ffn:
+                Fs = cfg.shared_ffn
+                b.add(p + "ffn_gate_shexp.weight", w(Fs, H), wt, threads)
+                b.add(p + "ffn_up_shexp.weight", w(Fs, H), wt, threads)
+                b.add(p + "ffn_down_shexp.weight", w(H, Fs), wt, threads)
+                if cfg.shared_gate:
+                    b.add(p + "ffn_gate_inp_shexp.weight", w(1, H), GgmlType.F32)
+        else:
+            b.add(p + "ffn_gate.weight", w(F, H), wt, threads)
+            b.add(p + "ffn_up.weight", w(F, H), wt, threads)
+            b.add(p + "ffn_down.weight", w(H, F), wt, threads)
+    b.add("output_norm.weight", np.ones(H, np.float32), GgmlType.F32)
+    if not cfg.tie_embeddings:
+        b.add("output.weight", w(cfg.vocab, H), wt, threads)
+    return b.write(path)
+
+
+def random_prompt(n: int, vocab: int, seed: int = 1) -> list:
+    """Uniform-random token ids (the benchmark prompts)."""
+    return np.random.default_rng(seed).integers(0, vocab, size=n).tolist()

@@ -1,0 +1,72 @@
+"""Builds the two in-tree native modules of hawking_b200.
+
+* ``hawking_b200._native``  host C++ (formats, CPU reference, engine, HTTP server); pybind11.
+* ``hawking_b200._kernels`` sm_100a CUDA kernels plus their torch bindings.
+
+Build in place (the .so files land next to the Python sources)::
+
+    python setup.py build_ext --inplace
+
+``HK_SKIP_CUDA=1`` builds only the host module.
+"""
+import glob
+import os
+
+import pybind11
+from setuptools import Extension, setup
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+CSRC = os.path.join("hawking_b200", "csrc")
+
+
+def _sources(*patterns):
+    out = []
+    for p in patterns:
+        out.extend(sorted(glob.glob(os.path.join(CSRC, p))))
+    return out
+
+
+CXX_FLAGS = ["-O3", "-std=c++17", "-pthread", "-fvisibility=hidden", "-Wno-unused-function"]
+
+ext_modules = [
+    Extension(
+        "hawking_b200._native",
+        sources=_sources("native/*.cpp", "bindings/native_module.cpp", "bindings/formats_bindings.cpp",
+                         "bindings/engine_bindings.cpp"),
+        include_dirs=[pybind11.get_include(), os.path.join(ROOT, CSRC)],
+        extra_compile_args=CXX_FLAGS,
+        extra_link_args=["-pthread"],
+        language="c++",
+    )
+]
+cmdclass = {}
+
+if os.environ.get("HK_SKIP_CUDA", "0") != "1":
+    from torch.utils.cpp_extension import BuildExtension, CUDAExtension
+
+    NVCC_FLAGS = [
+        "-O3", "-std=c++17", "-lineinfo",
+        "-gencode", "arch=compute_100a,code=sm_100a",
+        "--expt-relaxed-constexpr", "-Xptxas", "-v,-warn-spills" if os.environ.get("HK_PTXAS_V") else "-warn-spills",
+        "-DNDEBUG",
+    ]
+    if os.environ.get("HK_BOUNDS", "0") == "1":
+        NVCC_FLAGS.append("-DHK_BOUNDS=1")
+    ext_modules.append(
+        CUDAExtension(
+            "hawking_b200._kernels",
+            sources=_sources("kernels/*.cu", "bindings/kernels_module.cpp"),
+            include_dirs=[os.path.join(ROOT, CSRC, "kernels")],
+            extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
+            libraries=["cuda"],
+        )
+    )
+    cmdclass["build_ext"] = BuildExtension.with_options(use_ninja=True)
+
+setup(
+    name="hawking_b200",
+    version="0.1.0",
+    packages=["hawking_b200"],
+    ext_modules=ext_modules,
+    cmdclass=cmdclass,
+)
