@@ -1,0 +1,239 @@
+#!/usr/bin/env python
+"""Headline benchmark: decode tok/s at batch 1 (and batch 64) plus p50 TTFT at a 2k prompt, on the
+Llama-3-8B-arch GGUF Q4_K configuration, random-init weights, synthetic token ids.
+
+Contract (one JSON line on rank 0):
+  python bench.py --gpus N --steps K --warmup W [--impl reference]
+For N > 1 launch with torch.distributed.run (one rank per GPU, NCCL); the timed region is bracketed
+by a barrier + synchronize on both sides and the step time is the max over ranks.
+
+Timed ("value"): K back-to-back decode steps of B=1 sequence at context 2048, each step one CUDA
+graph replay of the whole forward (embedding -> 32 layers -> LM head -> argmax -> device-side
+input advance), timed with CUDA events. The 4.6 GB of weights streamed per step exceed the 126 MB
+L2, so no flush is needed between steps. "e2e": the same decode through the public Engine.step()
+API, including each step's pinned host->device input upload and the device->host read of the
+sampled id. TTFT: wall time from Engine.add_request to the first sampled token for a 2048-token
+prompt (engine prefill), p50 over runs.
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode tok/s bs1 & bs64 + p50 TTFT @2k prompt, 8×B200, max over ranks"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--model", default="llama3-8b")
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--ctx", type=int, default=2048)
+    ap.add_argument("--bs64", type=int, default=1, help="also time batch-64 decode (1/0)")
+    ap.add_argument("--ttft-runs", type=int, default=3)
+    ap.add_argument("--e2e-steps", type=int, default=0, help="0 = same as --steps")
+    ap.add_argument("--layers", type=int, default=0, help="override layer count (debug only; invalidates the number)")
+    return ap.parse_args()
+
+
+def reference_unavailable(args):
+    line = {"impl": "reference",
+            "unavailable": "the reference (joshuahickscorp/hawking) is a Rust+Metal workspace with no Python "
+                           "package; pip install of /root/reference fails (no setup.py/pyproject.toml) and Metal "
+                           "does not exist on this box"}
+    print(json.dumps(line))
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        if int(os.environ.get("RANK", "0")) == 0:
+            reference_unavailable(args)
+        return 0
+
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+
+    from hawking_b200 import ops
+    from hawking_b200.engine.engine import Engine
+    from hawking_b200.engine.sampling import SamplingParams
+    from hawking_b200.formats.synth import random_prompt
+    from hawking_b200.models.config import preset
+    from hawking_b200.models.llama import random_llama_weights
+    from hawking_b200.utils.clocks import ClockSampler
+
+    cfg = preset(args.model)
+    if args.layers:
+        cfg = cfg.with_(layers=args.layers)
+    B, ctx, K, W = args.batch, args.ctx, args.steps, args.warmup
+    max_ctx = ctx + 2 * (K + W) + 256
+    cfg = cfg.with_(max_ctx=max_ctx)
+    t0 = time.time()
+    w = random_llama_weights(cfg, dev, seed=0)
+    t_load = time.time() - t0
+    max_batch = max(B, 64 if args.bs64 else B)
+    eng = Engine.build(cfg, w, device=dev, max_batch=max_batch, max_ctx=max_ctx, block_size=64, max_rows=64,
+                       max_prefill_tokens=2048, kv_fraction=0.6)
+    m, kv = eng.model, eng.kv
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def setup_decode(nseq, first_id):
+        """nseq sequences holding `ctx` tokens of (random) KV, positioned for decode."""
+        ids, pos, rseq, rctx = [], [], [], []
+        for i in range(nseq):
+            sid = first_id + i
+            if not kv.bm.reserve(sid, ctx + K + W + 8):
+                raise RuntimeError("KV pool too small for the benchmark")
+            kv.sync_tables([sid])
+            ids.append(int(torch.randint(0, cfg.vocab, (1,)).item()))
+            pos.append(ctx)
+            rseq.append(kv.row(sid))
+            rctx.append(ctx + 1)
+        m.inp.upload(ids, pos, [0] * nseq, rseq, rctx)
+        return [first_id + i for i in range(nseq)]
+
+    def timed_decode(nseq):
+        for _ in range(W):
+            m.graph_forward(nseq, "greedy", advance=True)
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local) as cs:
+            e0.record()
+            for _ in range(K):
+                m.graph_forward(nseq, "greedy", advance=True)
+            e1.record()
+            torch.cuda.synchronize()
+        barrier()
+        ms = e0.elapsed_time(e1) / K
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = t.item()
+        return ms, cs.result
+
+    # Random KV content for the context (decode work does not depend on the values).
+    g = torch.Generator(device=dev).manual_seed(1)
+    for l in range(cfg.layers):
+        kv.k[l].normal_(0, 1, generator=g)
+        kv.v[l].normal_(0, 1, generator=g)
+
+    # ---- bs1 (or --batch) device-timed decode ----
+    seqs = setup_decode(B, 1_000_000)
+    ms1, clocks = timed_decode(B)
+    launches = m.launches_per_graph
+    for s in seqs:
+        kv.drop(s)
+    result_bs64 = None
+    if args.bs64 and B != 64:
+        seqs = setup_decode(64, 2_000_000)
+        ms64, clocks64 = timed_decode(64)
+        result_bs64 = {"tok_s_aggregate": round(64 * 1000.0 / ms64 * world, 1), "ms_per_step": round(ms64, 4),
+                       "clocks": clocks64}
+        for s in seqs:
+            kv.drop(s)
+    m.release_graphs()
+
+    # ---- TTFT @ctx prompt and e2e decode through the public API ----
+    ttfts = []
+    e2e = None
+    KE = args.e2e_steps or K
+    for run in range(max(1, args.ttft_runs)):
+        prompt = random_prompt(ctx, cfg.vocab, seed=100 + run)
+        torch.cuda.synchronize()
+        barrier()
+        t_a = time.perf_counter()
+        rid = eng.add_request(prompt, SamplingParams(max_tokens=KE + W + 1 if run == 0 else 1))
+        while not eng.requests[rid].output:
+            eng.step()
+        ttfts.append((time.perf_counter() - t_a) * 1000.0)
+        if run == 0:
+            for _ in range(W):
+                eng.step()
+            st = eng.stats
+            h0, d0 = st.h2d_bytes, st.d2h_bytes
+            torch.cuda.synchronize()
+            barrier()
+            t_e = time.perf_counter()
+            n0 = len(eng.requests[rid].output)
+            for _ in range(KE):
+                eng.step()
+            torch.cuda.synchronize()
+            dt = time.perf_counter() - t_e
+            n_tok = len(eng.requests[rid].output) - n0
+            if world > 1:
+                t = torch.tensor([dt], device=dev)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                dt = t.item()
+            e2e = {"value": round(n_tok * world / dt, 2), "unit": "tok/s",
+                   "h2d_bytes_per_step": (st.h2d_bytes - h0) // max(1, KE),
+                   "d2h_bytes_per_step": (st.d2h_bytes - d0) // max(1, KE),
+                   "api": "Engine.step()"}
+        while eng.has_work():
+            eng.step()
+    ttft_p50 = statistics.median(ttfts)
+
+    value = B * 1000.0 / ms1 * world
+    out = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": K,
+        "warmup": W,
+        "ms_per_step": round(ms1, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "q4_k weights, int8 activation blocks (W4A8 dp4a), fp32 accumulate, bf16 KV",
+        "data": "synthetic: random-init N(0,0.02) weights quantised to GGUF Q4_K on device; uniform-random "
+                "token ids; device-timed decode runs over a 2048-token KV context filled with random bf16",
+        "config": {"model": "llama3-8b (Llama-3-8B-arch: 32 layers, hidden 4096, 32/8 GQA heads, head_dim 128, "
+                            "FFN 14336, vocab 128256, rope theta 5e5, GGUF Q4_K)" + (
+                                f" [LAYERS OVERRIDDEN to {cfg.layers}]" if args.layers else ""),
+                   "global_batch": B * world, "seq_len": ctx,
+                   "parallelism": f"dp{world}" if world > 1 else "tp1",
+                   "l2": "inputs larger than L2: %.2f GB of weights streamed per step" % (w.nbytes / 1e9),
+                   "kv_block_size": 64},
+        "clocks": clocks,
+        "e2e": e2e,
+        "gpu_launches": launches * K,
+        "bs64": result_bs64,
+        "ttft_p50_ms": round(ttft_p50, 2),
+        "ttft_runs_ms": [round(t, 2) for t in ttfts],
+        "weights_gb": round(w.nbytes / 1e9, 3),
+        "weight_bw_gbs": round(w.nbytes / (ms1 * 1e-3) / 1e9, 1),
+        "load_s": round(t_load, 1),
+    }
+    if rank == 0:
+        print(json.dumps(out))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -182,6 +182,12 @@ PYBIND11_MODULE(_native, m) {
     for (size_t r = 0; r < rows; ++r) ref_rope(y.mutable_data() + r * hd, hd, rot_dim, pos, theta, style, nullptr);
     return y;
   });
+  m.def("ref_q8_roundtrip", [](py::array_t<float, py::array::c_style | py::array::forcecast> x) {
+    py::array_t<float> y(x.request().shape);
+    std::memcpy(y.mutable_data(), x.data(), sizeof(float) * x.size());
+    ref_q8_roundtrip(y.mutable_data(), (int)y.size());
+    return y;
+  });
   m.def("ref_topk_gate", [](py::array_t<float, py::array::c_style | py::array::forcecast> logits, int k, bool renorm) {
     int n = (int)logits.size();
     std::vector<int> ids(k);
@@ -210,10 +216,11 @@ PYBIND11_MODULE(_native, m) {
   py::class_<Pcg64>(m, "Pcg64").def(py::init<uint64_t>()).def("next_u64", &Pcg64::next_u64).def("next_f32", &Pcg64::next_f32);
 
   py::class_<CpuLlama>(m, "CpuLlama")
-      .def(py::init([](const std::string& path, int max_ctx, int threads) {
-             return new CpuLlama(std::shared_ptr<GgufFile>(GgufFile::open(path)), max_ctx, threads);
+      .def(py::init([](const std::string& path, int max_ctx, int threads, bool act_q8, bool bf16_kv) {
+             return new CpuLlama(std::shared_ptr<GgufFile>(GgufFile::open(path)), max_ctx, threads, act_q8, bf16_kv);
            }),
-           py::arg("path"), py::arg("max_ctx") = 2048, py::arg("threads") = 8)
+           py::arg("path"), py::arg("max_ctx") = 2048, py::arg("threads") = 8, py::arg("act_q8") = false,
+           py::arg("bf16_kv") = false)
       .def("forward", [](CpuLlama& m, int tok, int pos) {
         std::vector<float> l;
         {

@@ -1,0 +1,130 @@
+// Host-visible kernel API: argument structs and launch entry points of every kernel group.
+// Host-only code (the torch bindings) includes this header alone; device code is in the .cu/.cuh
+// files.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace hk {
+
+enum WFmt : int { WF_Q4_K = 12, WF_Q6_K = 14, WF_Q4_0 = 2, WF_Q5_0 = 6, WF_Q8_0 = 8 };
+
+struct WPlanes {
+  const uint8_t* p0;   // main plane (raw blocks / qs / ql)
+  const uint8_t* p1;   // scales plane (d), Q6_K: qh
+  const uint8_t* p2;   // Q5_0: qh ; Q6_K: sc
+  const uint8_t* p3;   // Q6_K: d
+  int64_t rb0, rb1, rb2, rb3;  // per-row byte strides of each plane
+};
+
+struct XQ {
+  const int8_t* q;  // [NB, K]
+  const float* d;   // [NB, K/32]
+  const float* s;   // [NB, K/32]
+  int64_t stride_q, stride_s;  // per-column strides (elements)
+};
+
+// ---- small-batch dequant GEMV (gemv.cu) ----
+
+enum GemvEpilogue : int { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU_Q8 = 2 };
+
+struct GemvArgs {
+  WPlanes w0, w1;          // w1 used by the SwiGLU pair epilogue (up projection)
+  int N, K;
+  const int8_t* xq;        // q8 activations [nb, K]
+  const float* xd;
+  const float* xs;
+  int64_t x_stride_q, x_stride_s;
+  float* y;                // [nb, y_stride] (STORE / RESID)
+  int64_t y_stride;
+  const float* bias;       // optional [N]
+  int8_t* oq;              // SWIGLU_Q8 output q8 [nb, N]
+  float* od;
+  float* os;
+  int64_t o_stride_q, o_stride_s;
+};
+
+void gemv_launch(int fmt, int epi, const GemvArgs& a, int nb, cudaStream_t s, bool pdl);
+
+// ---- decode ops (decode_ops.cu, attention.cu) ----
+
+// RMSNorm (optional weight) of rows of x, then q8 activation blocks. `norm=false` quantises x
+// unchanged. Also writes the normalised row to y (fp32) when y != nullptr.
+void rmsnorm_q8_launch(const float* x, int64_t x_stride, const float* w, float eps, bool norm, int rows, int K,
+                       int8_t* xq, float* xd, float* xs, float* y, cudaStream_t s, bool pdl);
+
+// Plain RMSNorm to bf16/fp32 (used ahead of tensor-core GEMMs).
+void rmsnorm_launch(const float* x, int64_t x_stride, const float* w, float eps, int rows, int K, float* y_f32,
+                    __nv_bfloat16* y_bf16, int64_t y_stride, cudaStream_t s, bool pdl);
+
+struct RopeAppendArgs {
+  const float* qkv;            // [R, (nh + 2*nkv) * hd] fp32 (projection output)
+  int64_t qkv_stride;
+  const float* bias;           // optional [(nh + 2*nkv) * hd]
+  const float* q_norm;         // optional per-head RMSNorm weights [hd] (Qwen3 style)
+  const float* k_norm;
+  float eps;
+  const int* positions;        // [R]
+  const int* slots;            // [R] paged slot = block * block_size + offset (-1 = skip); or null:
+  const int* block_tables;     //   slot from block_tables[row_seq[r], pos / bs] (when slots is null)
+  const int* row_seq;
+  int max_blocks;
+  const float* rope;           // [max_pos, rot/2, 2] (cos, sin)
+  int rot_dim, rope_style;     // 0 adjacent pairs, 1 neox halves
+  float* q_out;                // [R, nh, hd] fp32 (roped)
+  __nv_bfloat16* k_cache;      // [num_blocks, nkv, bs, hd]
+  __nv_bfloat16* v_cache;
+  int R, nh, nkv, hd, block_size;
+};
+void rope_append_launch(const RopeAppendArgs& a, cudaStream_t s, bool pdl);
+
+struct AttnDecodeArgs {
+  const float* q;              // [R, nh, hd] fp32, roped
+  const __nv_bfloat16* k_cache;
+  const __nv_bfloat16* v_cache;
+  const int* block_tables;     // [S, max_blocks]
+  int max_blocks;
+  const int* row_seq;          // [R] block-table row of each query row
+  const int* row_ctx;          // [R] number of keys visible to the row (causal length)
+  float scale;
+  int R, nh, nkv, hd, block_size, num_splits;
+  float* part_o;               // [R, nh, num_splits, hd] scratch
+  float* part_lse;             // [R, nh, num_splits] scratch
+  float* out;                  // [R, nh*hd] fp32 (optional)
+  int8_t* oq;                  // q8 output [R, nh*hd] (optional)
+  float* od;
+  float* os;
+  const float* sinks;          // optional per-head attention sink logits [nh]
+};
+void attention_decode_launch(const AttnDecodeArgs& a, cudaStream_t s, bool pdl);
+
+// Greedy: index of the max logit per row (lowest index on ties).
+void argmax_launch(const float* logits, int64_t stride, int rows, int V, int* out, cudaStream_t s, bool pdl);
+
+struct SampleArgs {
+  const float* logits;         // [R, V]
+  int64_t stride;
+  int R, V;
+  const float* temperature;    // [R]; <= 0 means greedy
+  const int* top_k;            // [R]; 0 = off (candidate pool capped at 1024)
+  const float* top_p;          // [R]
+  const float* rep_penalty;    // [R]
+  const int* recent;           // [R, recent_n] recent token ids (-1 = empty) for repetition penalty
+  int recent_n;
+  const float* uniforms;       // [R] uniform draws in [0,1)
+  int* out;                    // [R]
+};
+void sample_launch(const SampleArgs& a, cudaStream_t s, bool pdl);
+
+// Device-side step advance for back-to-back decode: ids <- next_ids, positions += 1, ctx += 1.
+void advance_launch(int* ids, const int* next_ids, int* positions, int* row_ctx, int R, cudaStream_t s, bool pdl);
+
+// Embedding rows: out[r] = dequant(table[ids[r]]) (fp32).
+void embed_launch(int fmt, const WPlanes& table, const int* ids, int R, int H, float* out, int64_t out_stride,
+                  cudaStream_t s, bool pdl);
+
+// ---- quantisers (quantize.cu) ----
+// n elements (rows * cols, cols a multiple of the block) -> planes p0..p3 of format fmt.
+void quantize_launch(int fmt, const float* x, int64_t n, void* p0, void* p1, void* p2, void* p3, cudaStream_t s);
+}  // namespace hk

@@ -1,0 +1,110 @@
+// Shared device helpers for the sm_100a kernels: conversions, warp reductions, programmatic
+// dependent launch (PDL) controls, launch helper and the device error word.
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdio>
+#include <stdexcept>
+#include <string>
+
+#define HK_CUDA_CHECK(expr)                                                                  \
+  do {                                                                                       \
+    cudaError_t _e = (expr);                                                                 \
+    if (_e != cudaSuccess)                                                                   \
+      throw std::runtime_error(std::string("CUDA error ") + cudaGetErrorString(_e) + " at " + \
+                               __FILE__ + ":" + std::to_string(__LINE__));                   \
+  } while (0)
+
+namespace hk {
+
+// Error codes written to the device status word (never trap: the host reads and reports).
+enum HkDeviceError : int {
+  HK_OK = 0,
+  HK_ERR_BOUNDS = 1,        // index guard failed (HK_BOUNDS builds)
+  HK_ERR_PEER_TIMEOUT = 2,  // bounded wait on a peer flag expired
+  HK_ERR_MBAR_TIMEOUT = 3,  // bounded wait on an mbarrier expired
+  HK_ERR_BAD_ARG = 4,
+};
+
+__device__ __forceinline__ void set_error(int* status, int code) {
+  if (status) atomicCAS(status, 0, code);
+}
+
+#if defined(HK_BOUNDS) && HK_BOUNDS
+#define HK_GUARD(cond, status) \
+  if (!(cond)) { ::hk::set_error((status), ::hk::HK_ERR_BOUNDS); return; }
+#else
+#define HK_GUARD(cond, status)
+#endif
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
+
+__device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+__device__ __forceinline__ float bf2f(uint16_t h) { return __uint_as_float(((uint32_t)h) << 16); }
+
+// Programmatic dependent launch: wait for the producing grid's memory, and let the next grid
+// start its prologue early. Both are no-ops when the launch has no PDL attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Cache-hinted streaming load (weights are read once per step: keep them out of L1).
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+// Block-wide sum over blockDim.x threads (<= 1024); `red` needs 32 floats of shared memory.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) red[w] = v;
+  __syncthreads();
+  v = lane < nw ? red[lane] : 0.f;
+  return warp_sum(v);
+}
+__device__ __forceinline__ float block_max(float v, float* red) {
+  int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  v = warp_max(v);
+  __syncthreads();
+  if (lane == 0) red[w] = v;
+  __syncthreads();
+  v = lane < nw ? red[lane] : -INFINITY;
+  return warp_max(v);
+}
+
+// Launch with the programmatic-stream-serialization attribute (PDL) when `pdl` is set.
+template <typename... KArgs, typename... Args>
+inline void launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                   bool pdl, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  HK_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...));
+}
+
+}  // namespace hk

@@ -1,0 +1,428 @@
+// Decode-path elementwise kernels: RMSNorm(+q8), RoPE + paged-KV append, argmax, sampling and
+// embedding lookup.
+//
+// Parity: crates/hawking-core/shaders/common.metal (rmsnorm, add_rmsnorm_fused_q8, rope variants,
+// kv append, embed lookup), crates/hawking-core/shaders/sample.metal (argmax, temperature,
+// repetition penalty, top-k, top-p, multinomial); CPU oracles crates/hawking-core/src/kernels/mod.rs:8-342
+// and crates/hawking-core/src/sample.rs:39-98.
+#include "decode_ops.cuh"
+
+namespace hk {
+
+// ---- RMSNorm + q8 --------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) rmsnorm_q8_kernel(const float* x, int64_t x_stride, const float* w, float eps,
+                                                          int norm, int K, int8_t* xq, float* xd, float* xs,
+                                                          float* y) {
+  __shared__ float red[32];
+  pdl_wait();
+  const int r = blockIdx.x;
+  const float* xr = x + (int64_t)r * x_stride;
+  float scale = 1.f;
+  if (norm) {
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < K; i += blockDim.x) ss += xr[i] * xr[i];
+    ss = block_sum(ss, red);
+    scale = rsqrtf(ss / K + eps);
+  }
+  pdl_launch();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int blk = warp; blk < K / 32; blk += nw) {
+    const int i = blk * 32 + lane;
+    float v = xr[i] * scale;
+    if (w) v *= w[i];
+    if (y) y[(int64_t)r * K + i] = v;
+    const float amax = warp_max(fabsf(v));
+    const float d = amax / 127.f;
+    const int q = amax > 0.f ? __float2int_rn(v / d) : 0;
+    const float qsum = warp_sum((float)q);
+    xq[(int64_t)r * K + i] = (int8_t)q;
+    if (lane == 0) {
+      xd[(int64_t)r * (K / 32) + blk] = d;
+      xs[(int64_t)r * (K / 32) + blk] = d * qsum;
+    }
+  }
+}
+
+void rmsnorm_q8_launch(const float* x, int64_t x_stride, const float* w, float eps, bool norm, int rows, int K,
+                       int8_t* xq, float* xd, float* xs, float* y, cudaStream_t s, bool pdl) {
+  if (K % 32) throw std::runtime_error("rmsnorm_q8: K must be a multiple of 32");
+  launch(rmsnorm_q8_kernel, dim3(rows), dim3(256), 0, s, pdl, x, x_stride, w, eps, (int)norm, K, xq, xd, xs, y);
+}
+
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const float* x, int64_t x_stride, const float* w, float eps,
+                                                       int K, float* yf, __nv_bfloat16* yb, int64_t y_stride) {
+  __shared__ float red[32];
+  pdl_wait();
+  const int r = blockIdx.x;
+  const float* xr = x + (int64_t)r * x_stride;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < K; i += blockDim.x) ss += xr[i] * xr[i];
+  ss = block_sum(ss, red);
+  const float scale = rsqrtf(ss / K + eps);
+  pdl_launch();
+  for (int i = threadIdx.x; i < K; i += blockDim.x) {
+    float v = xr[i] * scale * (w ? w[i] : 1.f);
+    if (yf) yf[(int64_t)r * y_stride + i] = v;
+    if (yb) yb[(int64_t)r * y_stride + i] = __float2bfloat16(v);
+  }
+}
+
+void rmsnorm_launch(const float* x, int64_t x_stride, const float* w, float eps, int rows, int K, float* y_f32,
+                    __nv_bfloat16* y_bf16, int64_t y_stride, cudaStream_t s, bool pdl) {
+  launch(rmsnorm_kernel, dim3(rows), dim3(256), 0, s, pdl, x, x_stride, w, eps, K, y_f32, y_bf16, y_stride);
+}
+
+// ---- RoPE + paged KV append -----------------------------------------------------------------
+// One CTA per query row; warp per head (q heads, then k heads, then v heads).
+__global__ void __launch_bounds__(256) rope_append_kernel(RopeAppendArgs a) {
+  pdl_wait();
+  const int r = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  const int pos = a.positions[r];
+  int64_t slot = -1;
+  if (a.slots) slot = a.slots[r];
+  else if (a.block_tables)
+    slot = (int64_t)a.block_tables[(int64_t)a.row_seq[r] * a.max_blocks + pos / a.block_size] * a.block_size +
+           pos % a.block_size;
+  const int hd = a.hd, half = a.rot_dim / 2;
+  const float* rope = a.rope + (int64_t)pos * half * 2;
+  const int nheads = a.nh + 2 * a.nkv;
+  for (int h = warp; h < nheads; h += nw) {
+    const int kind = h < a.nh ? 0 : (h < a.nh + a.nkv ? 1 : 2);  // q, k, v
+    const float* src = a.qkv + (int64_t)r * a.qkv_stride + (int64_t)h * hd;
+    const float* bias = a.bias ? a.bias + (int64_t)h * hd : nullptr;
+    float vals[8];  // hd <= 256
+    const int per = hd / 32;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (i < per) vals[i] = src[lane * per + i] + (bias ? bias[lane * per + i] : 0.f);
+    const float* nw_ = kind == 0 ? a.q_norm : (kind == 1 ? a.k_norm : nullptr);
+    if (nw_) {
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (i < per) ss += vals[i] * vals[i];
+      ss = warp_sum(ss);
+      const float sc = rsqrtf(ss / hd + a.eps);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (i < per) vals[i] *= sc * nw_[lane * per + i];
+    }
+    // Stage through shared memory so each lane can rotate any pair.
+    __shared__ float buf[8][256];
+    float* hb = buf[warp];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (i < per) hb[lane * per + i] = vals[i];
+    __syncwarp();
+    if (kind < 2) {
+      for (int p = lane; p < half; p += 32) {
+        const int ia = a.rope_style == 0 ? 2 * p : p;
+        const int ib = a.rope_style == 0 ? 2 * p + 1 : p + half;
+        const float c = rope[2 * p], sn = rope[2 * p + 1];
+        const float x0 = hb[ia], x1 = hb[ib];
+        hb[ia] = x0 * c - x1 * sn;
+        hb[ib] = x0 * sn + x1 * c;
+      }
+    }
+    __syncwarp();
+    if (kind == 0) {
+      float* dst = a.q_out + ((int64_t)r * a.nh + h) * hd;
+      for (int i = lane; i < hd; i += 32) dst[i] = hb[i];
+    } else if (slot >= 0) {
+      const int kh = kind == 1 ? h - a.nh : h - a.nh - a.nkv;
+      const int64_t blk = slot / a.block_size, off = slot % a.block_size;
+      __nv_bfloat16* cache = kind == 1 ? a.k_cache : a.v_cache;
+      __nv_bfloat16* dst = cache + ((blk * a.nkv + kh) * a.block_size + off) * hd;
+      for (int i = lane; i < hd; i += 32) dst[i] = __float2bfloat16(hb[i]);
+    }
+    __syncwarp();
+  }
+  pdl_launch();
+}
+
+void rope_append_launch(const RopeAppendArgs& a, cudaStream_t s, bool pdl) {
+  if (a.hd % 32 || a.hd > 256) throw std::runtime_error("rope_append: head_dim must be a multiple of 32, <= 256");
+  launch(rope_append_kernel, dim3(a.R), dim3(256), 0, s, pdl, a);
+}
+
+// ---- step advance ----------------------------------------------------------------------------
+__global__ void advance_kernel(int* ids, const int* next_ids, int* positions, int* row_ctx, int R) {
+  pdl_wait();
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r < R) {
+    ids[r] = next_ids[r];
+    positions[r] += 1;
+    row_ctx[r] += 1;
+  }
+}
+
+void advance_launch(int* ids, const int* next_ids, int* positions, int* row_ctx, int R, cudaStream_t s, bool pdl) {
+  launch(advance_kernel, dim3((R + 127) / 128), dim3(128), 0, s, pdl, ids, next_ids, positions, row_ctx, R);
+}
+
+// ---- argmax -----------------------------------------------------------------------------------
+__device__ __forceinline__ void argmax_merge(float& v, int& i, float v2, int i2) {
+  if (v2 > v || (v2 == v && i2 < i)) { v = v2; i = i2; }
+}
+
+__global__ void __launch_bounds__(1024) argmax_kernel(const float* logits, int64_t stride, int V, int* out) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  pdl_wait();
+  const float* l = logits + (int64_t)blockIdx.x * stride;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) argmax_merge(bv, bi, l[i], i);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float v2 = __shfl_xor_sync(0xffffffffu, bv, o);
+    int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+    argmax_merge(bv, bi, v2, i2);
+  }
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  if (lane == 0) { sv[w] = bv; si[w] = bi; }
+  __syncthreads();
+  if (w == 0) {
+    const int nw = blockDim.x >> 5;
+    bv = lane < nw ? sv[lane] : -INFINITY;
+    bi = lane < nw ? si[lane] : 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      float v2 = __shfl_xor_sync(0xffffffffu, bv, o);
+      int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+      argmax_merge(bv, bi, v2, i2);
+    }
+    if (lane == 0) out[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
+  }
+  pdl_launch();
+}
+
+void argmax_launch(const float* logits, int64_t stride, int rows, int V, int* out, cudaStream_t s, bool pdl) {
+  launch(argmax_kernel, dim3(rows), dim3(1024), 0, s, pdl, logits, stride, V, out);
+}
+
+// ---- sampling ---------------------------------------------------------------------------------
+// Order (as the CPU sampler): repetition penalty -> temperature (<=0: argmax) -> softmax over the
+// full vocabulary -> top-k -> top-p -> renormalise -> draw. Candidates are the top min(top_k,
+// 1024) logits, selected by a threshold search, then sorted with a bitonic sort in shared memory.
+constexpr int kCand = 1024;
+
+__device__ __forceinline__ float penalised(const float* l, int i, const int* recent, int rn, float pen) {
+  float v = l[i];
+  if (pen != 1.f)
+    for (int j = 0; j < rn; ++j)
+      if (recent[j] == i) { v = v >= 0.f ? v / pen : v * pen; break; }
+  return v;
+}
+
+__global__ void __launch_bounds__(1024) sample_kernel(SampleArgs a) {
+  __shared__ float red[32];
+  __shared__ float cv[kCand];
+  __shared__ int ci[kCand];
+  __shared__ int ccount;
+  __shared__ int hist[256];
+  pdl_wait();
+  const int r = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
+  const float* l = a.logits + (int64_t)r * a.stride;
+  const int* recent = a.recent ? a.recent + (int64_t)r * a.recent_n : nullptr;
+  const int rn = a.recent ? a.recent_n : 0;
+  const float pen = a.rep_penalty ? a.rep_penalty[r] : 1.f;
+  const float temp = a.temperature[r];
+  const int V = a.V;
+  // Greedy lane.
+  if (temp <= 0.f) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = tid; i < V; i += nt) argmax_merge(bv, bi, penalised(l, i, recent, rn, pen), i);
+    for (int o = 16; o > 0; o >>= 1) {
+      float v2 = __shfl_xor_sync(0xffffffffu, bv, o);
+      int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+      argmax_merge(bv, bi, v2, i2);
+    }
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    if ((tid & 31) == 0) { sv[tid >> 5] = bv; si[tid >> 5] = bi; }
+    __syncthreads();
+    if (tid < 32) {
+      bv = tid < (nt >> 5) ? sv[tid] : -INFINITY;
+      bi = tid < (nt >> 5) ? si[tid] : 0x7fffffff;
+      for (int o = 16; o > 0; o >>= 1) {
+        float v2 = __shfl_xor_sync(0xffffffffu, bv, o);
+        int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+        argmax_merge(bv, bi, v2, i2);
+      }
+      if (tid == 0) a.out[r] = bi;
+    }
+    return;
+  }
+  const float inv_t = 1.f / temp;
+  // Softmax normaliser over the full vocabulary.
+  float m = -INFINITY;
+  for (int i = tid; i < V; i += nt) m = fmaxf(m, penalised(l, i, recent, rn, pen) * inv_t);
+  m = block_max(m, red);
+  float z = 0.f;
+  for (int i = tid; i < V; i += nt) z += __expf(penalised(l, i, recent, rn, pen) * inv_t - m);
+  z = block_sum(z, red);
+  // Candidate threshold: find the 8-bit bucket (of the scaled logit distance from the max)
+  // containing the kc-th largest, refined once; then gather everything above it.
+  int kc = a.top_k && a.top_k[r] > 0 ? min(a.top_k[r], kCand) : kCand;
+  kc = min(kc, V);
+  // Threshold search on the distance from the max: a 256-bucket histogram over [0, 64), then one
+  // refinement inside the bucket that crosses kc. Tokens with distance below the threshold are the
+  // candidates (ties at the boundary beyond kCand are dropped).
+  __shared__ int sel_bucket, sel_before;
+  float lo = 0.f, hi = 64.f, thr_dist = 64.f;
+  for (int pass = 0; pass < 2; ++pass) {
+    for (int i = tid; i < 256; i += nt) hist[i] = 0;
+    __syncthreads();
+    const float bw = (hi - lo) / 256.f;
+    for (int i = tid; i < V; i += nt) {
+      const float dist = m - penalised(l, i, recent, rn, pen) * inv_t;
+      if (dist >= lo && dist < hi) atomicAdd(&hist[min(255, (int)((dist - lo) / bw))], 1);
+    }
+    __syncthreads();
+    if (tid == 0) {
+      int acc = 0, b = 0;
+      for (; b < 256; ++b) {
+        if (acc + hist[b] >= kc) break;
+        acc += hist[b];
+      }
+      sel_bucket = b;
+      sel_before = acc;
+    }
+    __syncthreads();
+    const int b = sel_bucket, before = sel_before;
+    const int inb = b < 256 ? hist[b] : 0;
+    __syncthreads();
+    if (b >= 256) { thr_dist = hi; break; }
+    thr_dist = lo + (b + 1) * bw;
+    if (before + inb == kc) break;
+    kc -= before;
+    hi = thr_dist;
+    lo = lo + b * bw;
+  }
+  __syncthreads();
+  if (tid == 0) ccount = 0;
+  __syncthreads();
+  for (int i = tid; i < V; i += nt) {
+    float x = penalised(l, i, recent, rn, pen) * inv_t;
+    if (m - x < thr_dist) {
+      int slot = atomicAdd(&ccount, 1);
+      if (slot < kCand) { cv[slot] = x; ci[slot] = i; }
+    }
+  }
+  __syncthreads();
+  const int nc = min(ccount, kCand);
+  for (int i = tid + nc; i < kCand; i += nt) { cv[i] = -INFINITY; ci[i] = 0x7fffffff; }
+  __syncthreads();
+  // Bitonic sort, descending by value then ascending index.
+  for (int k = 2; k <= kCand; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = tid; i < kCand; i += nt) {
+        int p = i ^ j;
+        if (p > i) {
+          bool desc = (i & k) == 0;
+          float vi = cv[i], vp = cv[p];
+          int ii = ci[i], ip = ci[p];
+          bool i_before_p = (vi > vp) || (vi == vp && ii < ip);
+          if (desc != i_before_p) { cv[i] = vp; cv[p] = vi; ci[i] = ip; ci[p] = ii; }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  if (tid == 0) {
+    int keep = nc;
+    if (a.top_k && a.top_k[r] > 0) keep = min(keep, a.top_k[r]);
+    const float tp = a.top_p ? a.top_p[r] : 1.f;
+    const float invz = 1.f / z;
+    if (tp > 0.f && tp < 1.f) {
+      float cum = 0.f;
+      for (int k = 0; k < keep; ++k) {
+        cum += __expf(cv[k] - m) * invz;
+        if (cum >= tp) { keep = k + 1; break; }
+      }
+    }
+    float total = 0.f;
+    for (int k = 0; k < keep; ++k) total += __expf(cv[k] - m) * invz;
+    const float u = a.uniforms[r] * total;
+    float acc = 0.f;
+    int pick = keep > 0 ? ci[keep - 1] : 0;
+    for (int k = 0; k < keep; ++k) {
+      acc += __expf(cv[k] - m) * invz;
+      if (u <= acc) { pick = ci[k]; break; }
+    }
+    a.out[r] = pick;
+  }
+  pdl_launch();
+}
+
+void sample_launch(const SampleArgs& a, cudaStream_t s, bool pdl) {
+  launch(sample_kernel, dim3(a.R), dim3(1024), 0, s, pdl, a);
+}
+
+// ---- embedding --------------------------------------------------------------------------------
+__device__ __forceinline__ float dequant_elem(int fmt, const WPlanes& t, int64_t row, int k) {
+  switch (fmt) {
+    case 0: return reinterpret_cast<const float*>(t.p0 + row * t.rb0)[k];
+    case 1: return __half2float(reinterpret_cast<const __half*>(t.p0 + row * t.rb0)[k]);
+    case 30: return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(t.p0 + row * t.rb0)[k]);
+    case WF_Q8_0: {
+      const int8_t q = reinterpret_cast<const int8_t*>(t.p0 + row * t.rb0)[k];
+      return __half2float(reinterpret_cast<const __half*>(t.p1 + row * t.rb1)[k >> 5]) * q;
+    }
+    case WF_Q4_0: {
+      const uint8_t b = (t.p0 + row * t.rb0)[(k >> 5) * 16 + (k & 15)];
+      const int q = (k & 16) ? (b >> 4) : (b & 0xF);
+      return __half2float(reinterpret_cast<const __half*>(t.p1 + row * t.rb1)[k >> 5]) * (q - 8);
+    }
+    case WF_Q5_0: {
+      const uint8_t b = (t.p0 + row * t.rb0)[(k >> 5) * 16 + (k & 15)];
+      const uint32_t qh = reinterpret_cast<const uint32_t*>(t.p2 + row * t.rb2)[k >> 5];
+      const int j = k & 31;
+      const int q = ((j & 16) ? (b >> 4) : (b & 0xF)) | (((qh >> j) & 1) << 4);
+      return __half2float(reinterpret_cast<const __half*>(t.p1 + row * t.rb1)[k >> 5]) * (q - 16);
+    }
+    case WF_Q4_K: {
+      const uint8_t* blk = t.p0 + row * t.rb0 + (int64_t)(k >> 8) * 144;
+      const int e = k & 255, j = e >> 5;  // sub-block
+      const uint32_t* s = reinterpret_cast<const uint32_t*>(blk + 4);
+      int sc, mn;
+      q4k_scale_min(j, s[0], s[1], s[2], sc, mn);
+      const uint8_t qb = blk[16 + (j >> 1) * 32 + (e & 31)];
+      const int q = (j & 1) ? (qb >> 4) : (qb & 0xF);
+      const float d = __half2float(reinterpret_cast<const __half*>(blk)[0]);
+      const float dmin = __half2float(reinterpret_cast<const __half*>(blk)[1]);
+      return d * sc * q - dmin * mn;
+    }
+    case WF_Q6_K: {
+      const int hb = k >> 7, e = k & 127, g = e >> 5, l = e & 31;
+      const uint8_t* ql = t.p0 + row * t.rb0 + (int64_t)hb * 64;
+      const uint8_t* qh = t.p1 + row * t.rb1 + (int64_t)hb * 32;
+      const int8_t* sc = reinterpret_cast<const int8_t*>(t.p2 + row * t.rb2) + hb * 8;
+      const float d = __half2float(reinterpret_cast<const __half*>(t.p3 + row * t.rb3)[k >> 8]);
+      const uint8_t lb = ql[l + ((g & 1) ? 32 : 0)];
+      const int lo = (g & 2) ? (lb >> 4) : (lb & 0xF);
+      const int q = (lo | (((qh[l] >> (2 * g)) & 3) << 4)) - 32;
+      return d * sc[2 * g + (l >> 4)] * q;
+    }
+  }
+  return 0.f;
+}
+
+__global__ void __launch_bounds__(256) embed_kernel(int fmt, WPlanes t, const int* ids, int H, float* out,
+                                                     int64_t out_stride) {
+  pdl_wait();
+  const int r = blockIdx.x;
+  const int64_t row = ids[r];
+  for (int k = threadIdx.x; k < H; k += blockDim.x) out[(int64_t)r * out_stride + k] = dequant_elem(fmt, t, row, k);
+  pdl_launch();
+}
+
+void embed_launch(int fmt, const WPlanes& table, const int* ids, int R, int H, float* out, int64_t out_stride,
+                  cudaStream_t s, bool pdl) {
+  launch(embed_kernel, dim3(R), dim3(256), 0, s, pdl, fmt, table, ids, H, out, out_stride);
+}
+
+}  // namespace hk

@@ -83,6 +83,15 @@ void ref_topk_gate(const float* logits, int n, int top_k, bool renorm, int* ids,
     for (int k = 0; k < top_k; ++k) w[k] /= s;
 }
 
+void ref_q8_roundtrip(float* x, int n) {
+  for (int b = 0; b + 32 <= n; b += 32) {
+    float amax = 0;
+    for (int i = 0; i < 32; ++i) amax = std::max(amax, std::fabs(x[b + i]));
+    float d = amax / 127.f;
+    for (int i = 0; i < 32; ++i) x[b + i] = amax > 0 ? (float)(int)std::nearbyint(x[b + i] / d) * d : 0.f;
+  }
+}
+
 int ref_argmax(const float* x, int n) {
   int best = 0;
   float bv = -INFINITY;
@@ -210,8 +219,8 @@ RefModelConfig ref_config_from_gguf(const GgufFile& f) {
   return c;
 }
 
-CpuLlama::CpuLlama(std::shared_ptr<GgufFile> file, int max_ctx, int threads)
-    : file_(std::move(file)), threads_(std::max(1, threads)) {
+CpuLlama::CpuLlama(std::shared_ptr<GgufFile> file, int max_ctx, int threads, bool act_q8, bool bf16_kv)
+    : file_(std::move(file)), threads_(std::max(1, threads)), act_q8_(act_q8), bf16_kv_(bf16_kv) {
   cfg_ = ref_config_from_gguf(*file_);
   cfg_.max_ctx = max_ctx;
   size_t per = (size_t)max_ctx * cfg_.n_kv_heads * cfg_.head_dim;
@@ -269,6 +278,7 @@ void CpuLlama::ffn_dense(int l, const float* xn, float* out) {
   matvec(g, xn, gv.data());
   matvec(u, xn, uv.data());
   ref_silu_mul(gv.data(), uv.data(), h.data(), g.rows);
+  if (act_q8_) ref_q8_roundtrip(h.data(), g.rows);
   matvec(d, h.data(), out);
 }
 
@@ -290,6 +300,7 @@ void CpuLlama::ffn_moe(int l, const float* xn, float* out) {
     matvec(ge, xn, gv.data(), (size_t)e * F, F);
     matvec(ue, xn, uv.data(), (size_t)e * F, F);
     ref_silu_mul(gv.data(), uv.data(), h.data(), F);
+    if (act_q8_) ref_q8_roundtrip(h.data(), F);
     Lin dd = de;
     dd.cols = F;
     matvec(dd, h.data(), o.data(), (size_t)e * H, H);
@@ -302,6 +313,7 @@ void CpuLlama::ffn_moe(int l, const float* xn, float* out) {
     matvec(gs, xn, g2.data());
     matvec(us, xn, u2.data());
     ref_silu_mul(g2.data(), u2.data(), h2.data(), gs.rows);
+    if (act_q8_) ref_q8_roundtrip(h2.data(), gs.rows);
     matvec(ds, h2.data(), o2.data());
     float gate = 1.f;
     Lin sg = lin(p + "ffn_gate_inp_shexp.weight", false);
@@ -330,6 +342,7 @@ std::vector<float> CpuLlama::forward(int token, int pos) {
     std::string p = "blk." + std::to_string(l) + ".";
     auto an = vec_f32(p + "attn_norm.weight");
     ref_rmsnorm(x.data(), an.data(), xn.data(), H, c.eps);
+    if (act_q8_) ref_q8_roundtrip(xn.data(), H);
     matvec(lin(p + "attn_q.weight"), xn.data(), q.data());
     matvec(lin(p + "attn_k.weight"), xn.data(), k.data());
     matvec(lin(p + "attn_v.weight"), xn.data(), v.data());
@@ -347,14 +360,18 @@ std::vector<float> CpuLlama::forward(int token, int pos) {
       if (!kn.empty()) ref_rmsnorm(&k[h * hd], kn.data(), &k[h * hd], hd, c.eps);
       ref_rope(&k[h * hd], hd, c.rot_dim, pos, c.theta, c.rope_style, ff);
     }
+    if (bf16_kv_)
+      for (int i = 0; i < nkv * hd; ++i) { k[i] = bf16_to_f32(f32_to_bf16(k[i])); v[i] = bf16_to_f32(f32_to_bf16(v[i])); }
     std::memcpy(&kc_[l][(size_t)pos * nkv * hd], k.data(), sizeof(float) * nkv * hd);
     std::memcpy(&vc_[l][(size_t)pos * nkv * hd], v.data(), sizeof(float) * nkv * hd);
     ref_attention_decode(q.data(), kc_[l].data(), vc_[l].data(), att.data(), nh, nkv, hd, pos + 1,
                          1.f / std::sqrt((float)hd));
+    if (act_q8_) ref_q8_roundtrip(att.data(), nh * hd);
     matvec(lin(p + "attn_output.weight"), att.data(), o.data());
     for (int i = 0; i < H; ++i) x[i] += o[i];
     auto fn = vec_f32(p + "ffn_norm.weight");
     ref_rmsnorm(x.data(), fn.data(), xn.data(), H, c.eps);
+    if (act_q8_) ref_q8_roundtrip(xn.data(), H);
     if (c.n_experts > 0) ffn_moe(l, xn.data(), o.data());
     else ffn_dense(l, xn.data(), o.data());
     for (int i = 0; i < H; ++i) x[i] += o[i];
@@ -362,6 +379,7 @@ std::vector<float> CpuLlama::forward(int token, int pos) {
   auto on = vec_f32("output_norm.weight");
   ref_rmsnorm(x.data(), on.data(), xn.data(), H, c.eps);
   last_hidden_ = xn;
+  if (act_q8_) ref_q8_roundtrip(xn.data(), H);
   Lin out = file_->find("output.weight") ? lin("output.weight") : lin("token_embd.weight");
   std::vector<float> logits(out.rows);
   matvec(out, xn.data(), logits.data());

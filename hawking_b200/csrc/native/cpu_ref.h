@@ -32,6 +32,8 @@ void ref_attention_decode(const float* q, const float* k, const float* v, float*
 // Softmax top-k gate with lowest-index tie break; returns (ids, weights).
 void ref_topk_gate(const float* logits, int n_experts, int top_k, bool renorm, int* ids, float* w);
 int ref_argmax(const float* x, int n);
+// Round-trip through q8 activation blocks (in place), n a multiple of 32.
+void ref_q8_roundtrip(float* x, int n);
 
 // PCG64-MCG-style 128-bit multiplicative generator used by the sampler.
 class Pcg64 {
@@ -78,7 +80,9 @@ RefModelConfig ref_config_from_gguf(const GgufFile& f);
 
 class CpuLlama {
  public:
-  CpuLlama(std::shared_ptr<GgufFile> file, int max_ctx, int threads);
+  // act_q8: round every matmul input to q8 activation blocks (int8 per 32, scale amax/127) and
+  // bf16_kv: store K/V rounded to bf16 — together they reproduce the device path's W4A8 numerics.
+  CpuLlama(std::shared_ptr<GgufFile> file, int max_ctx, int threads, bool act_q8 = false, bool bf16_kv = false);
   const RefModelConfig& config() const { return cfg_; }
   // Forward one token at position pos (positions must be fed in order). Returns logits.
   std::vector<float> forward(int token, int pos);
@@ -101,6 +105,7 @@ class CpuLlama {
   std::shared_ptr<GgufFile> file_;
   RefModelConfig cfg_;
   int threads_;
+  bool act_q8_ = false, bf16_kv_ = false;
   int n_past_ = 0;
   std::vector<std::vector<float>> kc_, vc_;  // per layer [max_ctx, n_kv, hd]
   std::vector<float> freq_factors_;

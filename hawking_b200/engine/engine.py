@@ -1,0 +1,210 @@
+"""The inference engine: model + paged KV + C++ scheduler, driven one step at a time.
+
+``Engine.step()`` asks the scheduler for a plan (decode rows for every running sequence plus
+budgeted prefill chunks), lays the plan out as forward rows, runs the model (decode-only steps
+replay a captured CUDA graph), samples on the device and reads back only the sampled ids
+(4 bytes per sequence), then commits the tokens to the scheduler.
+
+Parity: crates/hawking-core/src/engine.rs:352 (trait Engine: generate, prefill_slot,
+forward_multiseq_greedy_tokens :616, copy_kv_prefix_to_slot :600, embed :687),
+crates/hawking-serve/src/batch/driver.rs:52 (decode_ready_once: greedy token-only lane vs full-logits
+lane), crates/hawking-serve/src/lib.rs:785-1115 (prefill phase, decode phase, stream phase).
+"""
+from __future__ import annotations
+
+import itertools
+import time
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional
+
+import numpy as np
+import torch
+
+from .._ext import native
+from ..models.config import ModelConfig
+from .kv_cache import PagedKVCache
+from .sampling import RequestRng, SamplingParams
+
+
+@dataclass
+class RequestState:
+    id: int
+    params: SamplingParams
+    rng: RequestRng
+    output: List[int] = field(default_factory=list)
+    finish: int = 0
+    t_arrival: float = 0.0
+    t_first: Optional[float] = None
+    t_done: Optional[float] = None
+
+
+@dataclass
+class EngineStats:
+    steps: int = 0
+    decode_rows: int = 0
+    prefill_rows: int = 0
+    tokens_generated: int = 0
+    h2d_bytes: int = 0
+    d2h_bytes: int = 0
+    graph_steps: int = 0
+
+
+class Engine:
+    def __init__(self, cfg: ModelConfig, model, kv: PagedKVCache, max_batch: int = 8, max_prefill_tokens: int = 512,
+                 policy: int = 0, use_graphs: bool = True):
+        self.cfg, self.model, self.kv = cfg, model, kv
+        self.max_batch = max_batch
+        self.sched = native().Scheduler(kv.bm, max_batch, max_prefill_tokens, policy)
+        self.requests: Dict[int, RequestState] = {}
+        self._ids = itertools.count(1)
+        self.use_graphs = use_graphs
+        self.stats = EngineStats()
+        self._host_ids = torch.zeros(model.max_rows, dtype=torch.int32).pin_memory()
+
+    # ---- construction helpers ----
+    @staticmethod
+    def build(cfg: ModelConfig, weights, device="cuda", max_batch: int = 8, max_ctx: Optional[int] = None,
+              block_size: int = 64, num_blocks: Optional[int] = None, max_rows: int = 64,
+              max_prefill_tokens: int = 512, kv_fraction: float = 0.5, policy: int = 0):
+        from ..models.llama import LlamaModel
+        max_ctx = max_ctx or cfg.max_ctx
+        bpb = PagedKVCache.bytes_per_block(cfg.layers, cfg.n_kv_heads, cfg.head_dim, block_size)
+        if num_blocks is None:
+            free, _ = torch.cuda.mem_get_info(device)
+            num_blocks = int(free * kv_fraction // bpb)
+            num_blocks = min(num_blocks, max_batch * (-(-max_ctx // block_size)) + 16)
+        kv = PagedKVCache(cfg.layers, cfg.n_kv_heads, cfg.head_dim, num_blocks, block_size, max_batch,
+                          -(-max_ctx // block_size), device)
+        model = LlamaModel(cfg, weights, kv, max_rows=max(max_rows, max_batch), device=device)
+        return Engine(cfg, model, kv, max_batch=max_batch, max_prefill_tokens=max_prefill_tokens, policy=policy)
+
+    # ---- requests ----
+    def add_request(self, prompt: List[int], params: Optional[SamplingParams] = None) -> int:
+        params = params or SamplingParams()
+        rid = next(self._ids)
+        self.sched.add(rid, list(map(int, prompt)), params.max_tokens, params.greedy, list(params.stop_ids),
+                       self.cfg.max_ctx)
+        self.requests[rid] = RequestState(rid, params, RequestRng(params.seed), t_arrival=time.perf_counter())
+        return rid
+
+    def abort(self, rid: int):
+        self.sched.abort(rid)
+        self.kv.drop(rid)
+        st = self.requests.get(rid)
+        if st:
+            st.finish = 3
+
+    def has_work(self) -> bool:
+        return not self.sched.idle()
+
+    # ---- one step ----
+    def step(self) -> List[tuple]:
+        """Run one scheduler step. Returns [(request_id, token, finish_reason)] for sampled rows."""
+        plan = self.sched.schedule()
+        items = plan.items
+        if not items:
+            return []
+        m = self.model
+        ids, pos, slots, rseq, rctx, sample_rows = [], [], [], [], [], []
+        live = [it.id for it in items]
+        self.kv.sync_tables(live)
+        for it in items:
+            toks = self.sched.tokens(it.id)
+            r = self.kv.row(it.id)
+            sl = self.kv.bm.slots(it.id, it.p0, it.p1)
+            for p in range(it.p0, it.p1):
+                ids.append(toks[p])
+                pos.append(p)
+                rseq.append(r)
+                rctx.append(p + 1)
+            slots.extend(sl)
+            if it.sample:
+                sample_rows.append((it, len(ids) - 1))
+        n = len(ids)
+        decode_only = all(it.p1 - it.p0 == 1 for it in items)
+        greedy = all(it.greedy for it, _ in sample_rows)
+        mode = "greedy" if greedy else "none"
+        sampled: List[int] = []
+        R = m.max_rows
+        for c0 in range(0, n, R):
+            c1 = min(n, c0 + R)
+            self.stats.h2d_bytes += m.inp.upload(ids[c0:c1], pos[c0:c1], slots[c0:c1], rseq[c0:c1], rctx[c0:c1])
+            if self.use_graphs and decode_only and c1 - c0 == n:
+                m.graph_forward(c1 - c0, mode)
+                self.stats.graph_steps += 1
+            else:
+                m.forward(c1 - c0, mode)
+            rows_here = [(it, r - c0) for it, r in sample_rows if c0 <= r < c1]
+            if rows_here:
+                sampled.extend(self._sample(rows_here, greedy))
+        events = self.sched.commit(plan, sampled)
+        now = time.perf_counter()
+        out = []
+        for e in events:
+            st = self.requests.get(e.id)
+            if st is None or e.token < 0:
+                continue
+            st.output.append(e.token)
+            if st.t_first is None:
+                st.t_first = now
+            if e.finish:
+                st.finish = e.finish
+                st.t_done = now
+                self.kv.drop(e.id)
+            out.append((e.id, e.token, e.finish))
+        self.stats.steps += 1
+        self.stats.tokens_generated += len(sampled)
+        if decode_only:
+            self.stats.decode_rows += n
+        else:
+            self.stats.prefill_rows += n
+        return out
+
+    def _sample(self, rows_here, greedy: bool) -> List[int]:
+        m = self.model
+        idx = [r for _, r in rows_here]
+        if greedy:
+            k = len(idx)
+            if idx == list(range(idx[0], idx[0] + k)):
+                self._host_ids[:k].copy_(m.next_ids[idx[0]:idx[0] + k], non_blocking=True)
+            else:
+                self._host_ids[:k].copy_(m.next_ids[torch.tensor(idx, device=m.dev)], non_blocking=True)
+            torch.cuda.current_stream(m.dev).synchronize()
+            self.stats.d2h_bytes += 4 * k
+            return self._host_ids[:k].tolist()
+        # full-logits lane: device sampler for temperature / top-k / top-p; repetition penalty on host
+        out = []
+        for it, r in rows_here:
+            st = self.requests[it.id]
+            p = st.params
+            if p.temperature <= 0.0 and p.repetition_penalty == 1.0:
+                torch.cuda.current_stream(m.dev).synchronize()
+                out.append(int(torch.argmax(m.logits[r]).item()))
+                continue
+            if p.repetition_penalty != 1.0:
+                logits = m.logits[r].float().cpu().numpy()
+                s = native().Sampler(p.seed)
+                for t in self.sched.tokens(it.id)[-64:]:
+                    s.record(t)
+                sp = native().SamplingParams()
+                sp.temperature, sp.top_k, sp.top_p, sp.repetition_penalty = p.temperature, p.top_k, p.top_p, p.repetition_penalty
+                out.append(int(s.sample(logits, sp)))
+                self.stats.d2h_bytes += logits.nbytes
+                continue
+            m.temperature[r] = p.temperature
+            m.top_k[r] = p.top_k
+            m.top_p[r] = p.top_p
+            m.uniforms[r] = st.rng.uniform()
+            from .. import ops
+            ops.sample(m.logits[r:r + 1], m.temperature[r:r + 1], m.top_k[r:r + 1], m.top_p[r:r + 1], None, None,
+                       m.uniforms[r:r + 1], m.next_ids[r:r + 1])
+            out.append(int(m.next_ids[r].item()))
+            self.stats.d2h_bytes += 4
+        return out
+
+    # ---- convenience ----
+    def generate(self, prompts: List[List[int]], params: Optional[SamplingParams] = None) -> List[List[int]]:
+        rids = [self.add_request(p, params) for p in prompts]
+        while self.has_work():
+            self.step()
+        return [self.requests[r].output for r in rids]

@@ -1,0 +1,121 @@
+"""Python surface of the sm_100a kernels. Each function launches on the current CUDA stream.
+
+The kernel module must be built (``python setup.py build_ext --inplace``); there is no eager
+fallback on a GPU machine.
+"""
+from __future__ import annotations
+
+import os
+from typing import Optional
+
+import torch
+
+from .._ext import kernels
+from .qweight import QWeight, cat_rows  # noqa: F401
+
+PDL = os.environ.get("HK_PDL", "1") == "1"
+
+EPI_STORE, EPI_RESID, EPI_SWIGLU_Q8 = 0, 1, 2
+
+
+class _LaunchCounter:
+    """Counts kernel launches issued through this module (per captured step)."""
+
+    def __init__(self):
+        self.n = 0
+
+    def add(self, k: int = 1):
+        self.n += k
+
+
+launches = _LaunchCounter()
+
+
+class Q8Act:
+    """q8 activation blocks for ``rows`` rows of width ``K``: int8 quants + fp32 scale/sum."""
+
+    def __init__(self, rows: int, K: int, device):
+        self.K = K
+        self.q = torch.zeros(rows, K, dtype=torch.int8, device=device)
+        self.d = torch.zeros(rows, K // 32, dtype=torch.float32, device=device)
+        self.s = torch.zeros(rows, K // 32, dtype=torch.float32, device=device)
+
+    def view(self, n: int) -> "Q8Act":
+        v = Q8Act.__new__(Q8Act)
+        v.K, v.q, v.d, v.s = self.K, self.q[:n], self.d[:n], self.s[:n]
+        return v
+
+    def dequantize(self) -> torch.Tensor:
+        return self.q.float() * self.d.repeat_interleave(32, dim=1)
+
+
+def rmsnorm_q8(x: torch.Tensor, w: Optional[torch.Tensor], eps: float, out: Q8Act, norm: bool = True,
+               y: Optional[torch.Tensor] = None):
+    launches.add()
+    kernels().rmsnorm_q8(x, w, eps, norm, out.q, out.d, out.s, y, PDL)
+
+
+def rmsnorm(x, w, eps, yf=None, yb=None):
+    launches.add()
+    kernels().rmsnorm(x, w, eps, yf, yb, PDL)
+
+
+def gemv(w: QWeight, x: Q8Act, y: torch.Tensor, residual: bool = False, bias=None):
+    launches.add()
+    kernels().gemv(w.fmt, EPI_RESID if residual else EPI_STORE, w.planes, [], w.N, w.K, x.q, x.d, x.s, y, bias,
+                   None, None, None, PDL)
+
+
+def gemv_swiglu(w_gate: QWeight, w_up: QWeight, x: Q8Act, out: Q8Act):
+    launches.add()
+    kernels().gemv(w_gate.fmt, EPI_SWIGLU_Q8, w_gate.planes, w_up.planes, w_gate.N, w_gate.K, x.q, x.d, x.s, None,
+                   None, out.q, out.d, out.s, PDL)
+
+
+def rope_table(max_pos: int, rot_dim: int, theta: float, freq_factors: Optional[torch.Tensor] = None,
+               device="cuda") -> torch.Tensor:
+    """[max_pos, rot_dim/2, 2] (cos, sin), computed in float64."""
+    half = rot_dim // 2
+    i = torch.arange(half, dtype=torch.float64)
+    freq = theta ** (-2.0 * i / rot_dim)
+    if freq_factors is not None:
+        freq = freq / freq_factors.double().cpu()
+    ang = torch.arange(max_pos, dtype=torch.float64)[:, None] * freq[None, :]
+    return torch.stack([torch.cos(ang), torch.sin(ang)], -1).float().to(device)
+
+
+def rope_append(qkv, positions, slots, rope, rot_dim, style, q_out, k_cache, v_cache, nh, nkv, hd, block_size,
+                bias=None, q_norm=None, k_norm=None, eps=1e-6, block_tables=None, row_seq=None):
+    """RoPE q/k (optional bias and per-head q/k RMSNorm) and append k/v to the paged cache at
+    ``slots`` (or, when slots is None, at the slot the block table maps each row's position to)."""
+    launches.add()
+    kernels().rope_append(qkv, bias, q_norm, k_norm, eps, positions, slots, rope, rot_dim, style, q_out, k_cache,
+                          v_cache, nh, nkv, hd, block_size, block_tables, row_seq, PDL)
+
+
+def advance(ids, next_ids, positions, row_ctx, rows: int):
+    launches.add()
+    kernels().advance(ids, next_ids, positions, row_ctx, rows, PDL)
+
+
+def attention_decode(q, k_cache, v_cache, block_tables, row_seq, row_ctx, scale, num_splits, part_o, part_lse,
+                     out=None, out_q8: Optional[Q8Act] = None, sinks=None):
+    launches.add(2)
+    kernels().attention_decode(q, k_cache, v_cache, block_tables, row_seq, row_ctx, scale, num_splits, part_o,
+                               part_lse, out, out_q8.q if out_q8 else None, out_q8.d if out_q8 else None,
+                               out_q8.s if out_q8 else None, sinks, PDL)
+
+
+def argmax(logits: torch.Tensor, out: torch.Tensor):
+    launches.add()
+    kernels().argmax(logits, out, PDL)
+
+
+def sample(logits, temperature, top_k, top_p, rep_penalty, recent, uniforms, out):
+    launches.add()
+    kernels().sample(logits, temperature, top_k, top_p, rep_penalty, recent, uniforms, out, PDL)
+
+
+def embed(table: QWeight, ids: torch.Tensor, out: torch.Tensor):
+    launches.add()
+    kernels().embed(table.fmt, table.planes, ids, out, PDL)

@@ -1,0 +1,191 @@
+"""Numerics of the sm_100a decode kernels against plain-PyTorch fp32 references."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+from hawking_b200 import ops  # noqa: E402
+from hawking_b200.formats.ggml import GgmlType  # noqa: E402
+from hawking_b200.models.torch_ref import rope_ref  # noqa: E402
+from hawking_b200.ops import Q8Act, QWeight  # noqa: E402
+
+DEV = "cuda"
+FORMATS = [GgmlType.Q4_K, GgmlType.Q6_K, GgmlType.Q4_0, GgmlType.Q8_0]
+
+
+def _q8(x: torch.Tensor) -> Q8Act:
+    a = Q8Act(x.shape[0], x.shape[1], DEV)
+    ops.rmsnorm_q8(x.contiguous(), None, 0.0, a, norm=False)
+    return a
+
+
+@pytest.mark.parametrize("fmt", FORMATS)
+def test_gpu_quantize_matches_cpu_bytes(native, fmt):
+    x = torch.randn(64, 512, generator=torch.Generator().manual_seed(3)) * 0.05
+    w = QWeight.quantize(x.to(DEV), fmt)
+    cpu = native.quantize_rows(fmt, x.numpy())
+    np.testing.assert_array_equal(w.to_raw().cpu().numpy(), cpu)
+
+
+def test_q8_activation_quant():
+    x = torch.randn(3, 512, device=DEV)
+    a = _q8(x)
+    blocks = x.view(3, 16, 32)
+    d = blocks.abs().amax(-1) / 127
+    q = torch.round(blocks / d[..., None])
+    torch.testing.assert_close(a.d, d)
+    assert (a.q.float().view(3, 16, 32) - q).abs().max() <= 1
+    torch.testing.assert_close(a.s, d * a.q.float().view(3, 16, 32).sum(-1))
+
+
+@pytest.mark.parametrize("fmt", FORMATS + [GgmlType.Q5_0])
+@pytest.mark.parametrize("nb", [1, 3, 8])
+def test_gemv_matches_fp32_reference(fmt, nb):
+    g = torch.Generator(device=DEV).manual_seed(int(fmt) * 10 + nb)
+    N, K = 320, 1024
+    w = QWeight.quantize(torch.randn(N, K, device=DEV, generator=g) * 0.02, fmt)
+    x = torch.randn(nb, K, device=DEV, generator=g)
+    a = _q8(x)
+    y = torch.zeros(nb, N, device=DEV)
+    ops.gemv(w, a, y)
+    ref = a.dequantize() @ w.dequantize().T
+    torch.testing.assert_close(y, ref, rtol=1e-4, atol=1e-4 * ref.abs().max().item())
+    # residual epilogue accumulates
+    y2 = y.clone()
+    ops.gemv(w, a, y2, residual=True)
+    torch.testing.assert_close(y2, 2 * ref, rtol=1e-4, atol=2e-4 * ref.abs().max().item())
+
+
+@pytest.mark.parametrize("fmt", [GgmlType.Q4_K, GgmlType.Q4_0])
+def test_gemv_swiglu_q8(fmt):
+    g = torch.Generator(device=DEV).manual_seed(5)
+    F, K, nb = 256, 512, 2
+    wg = QWeight.quantize(torch.randn(F, K, device=DEV, generator=g) * 0.05, fmt)
+    wu = QWeight.quantize(torch.randn(F, K, device=DEV, generator=g) * 0.05, fmt)
+    a = _q8(torch.randn(nb, K, device=DEV, generator=g))
+    out = Q8Act(nb, F, DEV)
+    ops.gemv_swiglu(wg, wu, a, out)
+    xd = a.dequantize()
+    gate, up = xd @ wg.dequantize().T, xd @ wu.dequantize().T
+    h = torch.nn.functional.silu(gate) * up
+    got = out.dequantize()
+    tol = out.d.repeat_interleave(32, 1) * 0.51 + 1e-6
+    assert ((got - h).abs() <= tol + 1e-4 * h.abs()).all()
+
+
+def test_rmsnorm_q8_matches():
+    x = torch.randn(4, 1024, device=DEV)
+    w = torch.rand(1024, device=DEV) + 0.5
+    a = Q8Act(4, 1024, DEV)
+    y = torch.zeros(4, 1024, device=DEV)
+    ops.rmsnorm_q8(x, w, 1e-5, a, y=y)
+    ref = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + 1e-5) * w
+    torch.testing.assert_close(y, ref, rtol=1e-5, atol=1e-5)
+    assert ((a.dequantize() - ref).abs() <= a.d.repeat_interleave(32, 1) * 0.51 + 1e-6).all()
+
+
+@pytest.mark.parametrize("style", [0, 1])
+@pytest.mark.parametrize("hd", [64, 128])
+def test_rope_append(style, hd):
+    nh, nkv, R, bs = 4, 2, 3, 16
+    qkv = torch.randn(R, (nh + 2 * nkv) * hd, device=DEV)
+    pos = torch.tensor([0, 5, 37], dtype=torch.int32, device=DEV)
+    slots = torch.tensor([3, 17, 40], dtype=torch.int32, device=DEV)
+    rope = ops.rope_table(64, hd, 10000.0, device=DEV)
+    q = torch.zeros(R, nh, hd, device=DEV)
+    kc = torch.zeros(4, nkv, bs, hd, dtype=torch.bfloat16, device=DEV)
+    vc = torch.zeros_like(kc)
+    ops.rope_append(qkv, pos, slots, rope, hd, style, q, kc, vc, nh, nkv, hd, bs)
+    qr = rope_ref(qkv[:, : nh * hd].view(R, nh, hd), pos.long(), 10000.0, hd, style)
+    kr = rope_ref(qkv[:, nh * hd:(nh + nkv) * hd].view(R, nkv, hd), pos.long(), 10000.0, hd, style)
+    torch.testing.assert_close(q, qr, rtol=1e-5, atol=1e-5)
+    for r, s in enumerate(slots.tolist()):
+        torch.testing.assert_close(kc[s // bs, :, s % bs].float(), kr[r].bfloat16().float())
+        torch.testing.assert_close(vc[s // bs, :, s % bs].float(),
+                                   qkv[r, (nh + nkv) * hd:].view(nkv, hd).bfloat16().float())
+
+
+def _paged_attention_ref(q, kc, vc, tables, row_seq, row_ctx, scale):
+    R, nh, hd = q.shape
+    nkv, bs = kc.shape[1], kc.shape[2]
+    out = torch.zeros(R, nh, hd, device=q.device)
+    for r in range(R):
+        n = int(row_ctx[r])
+        blocks = tables[int(row_seq[r])]
+        ks = torch.stack([kc[blocks[t // bs], :, t % bs] for t in range(n)]).float()  # [n, nkv, hd]
+        vs = torch.stack([vc[blocks[t // bs], :, t % bs] for t in range(n)]).float()
+        g = nh // nkv
+        K = ks.repeat_interleave(g, 1)
+        V = vs.repeat_interleave(g, 1)
+        s = torch.einsum("hd,thd->ht", q[r], K) * scale
+        out[r] = torch.einsum("ht,thd->hd", torch.softmax(s, -1), V)
+    return out
+
+
+@pytest.mark.parametrize("nh,nkv,hd", [(8, 2, 64), (32, 8, 128), (16, 2, 256), (8, 8, 128)])
+@pytest.mark.parametrize("splits", [1, 7])
+def test_attention_decode(nh, nkv, hd, splits):
+    g = torch.Generator(device=DEV).manual_seed(nh + hd + splits)
+    bs, nblk = 16, 40
+    kc = torch.randn(nblk, nkv, bs, hd, device=DEV, generator=g).bfloat16()
+    vc = torch.randn(nblk, nkv, bs, hd, device=DEV, generator=g).bfloat16()
+    perm = torch.randperm(nblk, device=DEV, generator=g).int()
+    tables = torch.stack([perm[:20], perm[20:]]).contiguous()
+    row_seq = torch.tensor([0, 1, 0], dtype=torch.int32, device=DEV)
+    row_ctx = torch.tensor([1, 100, 319], dtype=torch.int32, device=DEV)
+    R = 3
+    q = torch.randn(R, nh, hd, device=DEV, generator=g)
+    scale = 1 / math.sqrt(hd)
+    part_o = torch.zeros(R * nh * splits * hd, device=DEV)
+    part_l = torch.zeros(R * nh * splits, device=DEV)
+    out = torch.zeros(R, nh * hd, device=DEV)
+    oq = Q8Act(R, nh * hd, DEV)
+    ops.attention_decode(q, kc, vc, tables, row_seq, row_ctx, scale, splits, part_o, part_l, out=out, out_q8=oq)
+    ref = _paged_attention_ref(q, kc, vc, tables, row_seq, row_ctx, scale).reshape(R, -1)
+    torch.testing.assert_close(out, ref, rtol=2e-3, atol=2e-3)
+    assert ((oq.dequantize() - ref).abs() <= oq.d.repeat_interleave(32, 1) * 0.51 + 3e-3).all()
+
+
+def test_argmax_lowest_index_on_ties():
+    l = torch.randn(3, 50000, device=DEV)
+    l[0, 100] = 9.0
+    l[0, 40000] = 9.0
+    l[1, 49999] = 12.0
+    out = torch.zeros(3, dtype=torch.int32, device=DEV)
+    ops.argmax(l, out)
+    assert out.tolist() == [100, 49999, int(torch.argmax(l[2]))]
+
+
+def test_sampler_topk1_and_distribution():
+    V = 32000
+    l = torch.randn(2, V, device=DEV)
+    temp = torch.tensor([1.0, 1.0], device=DEV)
+    topk = torch.tensor([1, 0], dtype=torch.int32, device=DEV)
+    topp = torch.tensor([1.0, 0.9], device=DEV)
+    out = torch.zeros(2, dtype=torch.int32, device=DEV)
+    u = torch.tensor([0.7, 0.3], device=DEV)
+    ops.sample(l, temp, topk, topp, None, None, u, out)
+    assert out[0].item() == int(torch.argmax(l[0]))
+    # row 1: compare with an exact CPU implementation of the same draw
+    p = torch.softmax(l[1].double(), -1)
+    order = torch.argsort(p, descending=True, stable=True)
+    cum = torch.cumsum(p[order], 0)
+    keep = int((cum < 0.9).sum().item()) + 1
+    total = p[order[:keep]].sum()
+    r = 0.3 * total
+    idx = int(torch.searchsorted(torch.cumsum(p[order[:keep]], 0), r).item())
+    assert out[1].item() == int(order[min(idx, keep - 1)])
+
+
+@pytest.mark.parametrize("fmt", [GgmlType.Q4_K, GgmlType.Q8_0, GgmlType.Q4_0, GgmlType.Q6_K, GgmlType.F16])
+def test_embed(fmt):
+    V, H = 64, 512
+    table = torch.randn(V, H, device=DEV) * 0.1
+    w = QWeight.quantize(table, fmt)
+    ids = torch.tensor([0, 63, 17], dtype=torch.int32, device=DEV)
+    out = torch.zeros(3, H, device=DEV)
+    ops.embed(w, ids, out)
+    torch.testing.assert_close(out, w.dequantize()[ids.long()], rtol=0, atol=1e-6)
