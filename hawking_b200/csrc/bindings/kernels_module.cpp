@@ -138,7 +138,7 @@ void attention_decode(const Tensor& q, const Tensor& k_cache, const Tensor& v_ca
                       const Tensor& row_seq, const Tensor& row_ctx, double scale, int64_t num_splits,
                       const Tensor& part_o, const Tensor& part_lse, const optional<Tensor>& out,
                       const optional<Tensor>& oq, const optional<Tensor>& od, const optional<Tensor>& os,
-                      const optional<Tensor>& sinks, bool pdl) {
+                      const optional<Tensor>& sinks, const optional<Tensor>& out_bf16, bool pdl) {
   check_cuda(q, "q");
   TORCH_CHECK(q.dim() == 3 && q.scalar_type() == at::kFloat, "q must be fp32 [R, nh, hd]");
   TORCH_CHECK(k_cache.dim() == 4 && k_cache.scalar_type() == at::kBFloat16, "k_cache must be bf16 [blocks, nkv, bs, hd]");
@@ -169,6 +169,7 @@ void attention_decode(const Tensor& q, const Tensor& k_cache, const Tensor& v_ca
   a.od = optr<float>(od);
   a.os = optr<float>(os);
   a.sinks = optr<float>(sinks);
+  a.out_bf16 = optr<__nv_bfloat16>(out_bf16);
   const c10::cuda::CUDAGuard g(q.device());
   hk::attention_decode_launch(a, cur_stream(), pdl);
 }
@@ -237,7 +238,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("block_tables"), py::arg("row_seq"), py::arg("row_ctx"), py::arg("scale"), py::arg("num_splits"),
         py::arg("part_o"), py::arg("part_lse"), py::arg("out") = py::none(), py::arg("oq") = py::none(),
         py::arg("od") = py::none(), py::arg("os") = py::none(), py::arg("sinks") = py::none(),
-        py::arg("pdl") = false);
+        py::arg("out_bf16") = py::none(), py::arg("pdl") = false);
   m.def("argmax", &argmax, py::arg("logits"), py::arg("out"), py::arg("pdl") = false);
   m.def("sample", &sample, py::arg("logits"), py::arg("temperature"), py::arg("top_k"), py::arg("top_p"),
         py::arg("rep_penalty"), py::arg("recent"), py::arg("uniforms"), py::arg("out"), py::arg("pdl") = false);

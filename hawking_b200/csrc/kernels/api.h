@@ -96,6 +96,7 @@ struct AttnDecodeArgs {
   float* od;
   float* os;
   const float* sinks;          // optional per-head attention sink logits [nh]
+  __nv_bfloat16* out_bf16;     // optional [R, nh*hd] bf16 output (tensor-core GEMM path)
 };
 void attention_decode_launch(const AttnDecodeArgs& a, cudaStream_t s, bool pdl);
 
@@ -123,6 +124,32 @@ void advance_launch(int* ids, const int* next_ids, int* positions, int* row_ctx,
 // Embedding rows: out[r] = dequant(table[ids[r]]) (fp32).
 void embed_launch(int fmt, const WPlanes& table, const int* ids, int R, int H, float* out, int64_t out_stride,
                   cudaStream_t s, bool pdl);
+
+// ---- tensor-core dequant GEMM (gemm_tc.cu) ----
+struct TcGemmArgs {
+  int fmt;                      // weight format (Q4_K)
+  const uint8_t* w;             // raw blocks [N, w_row_bytes]
+  int64_t w_row_bytes;
+  int N, K;
+  const __nv_bfloat16* x;       // [M, x_stride] bf16
+  int64_t x_stride;
+  int M;
+  float* y;                     // [M, y_stride] fp32
+  int64_t y_stride;
+  int atomic;                   // accumulate into y (residual / split-K)
+  int y_zeroed;                 // caller zeroed y (allows split-K with a plain result)
+  int k_splits;
+  int bn;                       // token tile: 32, 64 or 128
+  int* status;                  // device status word (bounded-wait errors)
+  bool pdl;
+};
+int tc_gemm_splits(int N, int M, int K, int bn, int sms);
+void tc_gemm_launch(const TcGemmArgs& g, cudaStream_t s);
+
+// SwiGLU over a fused [gate | up] fp32 GEMM output: h = silu(g) * u -> bf16, then zero the input
+// (ready for the next split-K accumulation).
+void swiglu_bf16_launch(float* gu, int64_t gu_stride, int M, int F, __nv_bfloat16* h, int64_t h_stride,
+                        bool clear, cudaStream_t s, bool pdl);
 
 // ---- quantisers (quantize.cu) ----
 // n elements (rows * cols, cols a multiple of the block) -> planes p0..p3 of format fmt.

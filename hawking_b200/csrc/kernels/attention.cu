@@ -215,6 +215,10 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(AttnDecodeArgs a) {
 #pragma unroll
     for (int i = 0; i < HPL; ++i) a.out[(int64_t)r * width + col0 + i] = o[i];
   }
+  if (a.out_bf16) {
+#pragma unroll
+    for (int i = 0; i < HPL; ++i) a.out_bf16[(int64_t)r * width + col0 + i] = __float2bfloat16(o[i]);
+  }
   if (a.oq) {
     // A q8 block of 32 dims spans 32/HPL lanes.
     float amax = 0.f;

@@ -146,6 +146,26 @@ void rope_append_launch(const RopeAppendArgs& a, cudaStream_t s, bool pdl) {
   launch(rope_append_kernel, dim3(a.R), dim3(256), 0, s, pdl, a);
 }
 
+// ---- SwiGLU over a fused gate|up GEMM output ---------------------------------------------------
+__global__ void __launch_bounds__(256) swiglu_bf16_kernel(float* gu, int64_t gs, int F, __nv_bfloat16* h,
+                                                           int64_t hs, int clear) {
+  pdl_wait();
+  const int m = blockIdx.y;
+  float* g = gu + (int64_t)m * gs;
+  for (int f = blockIdx.x * blockDim.x + threadIdx.x; f < F; f += gridDim.x * blockDim.x) {
+    const float gv = g[f], uv = g[F + f];
+    h[(int64_t)m * hs + f] = __float2bfloat16(gv / (1.f + __expf(-gv)) * uv);
+    if (clear) { g[f] = 0.f; g[F + f] = 0.f; }
+  }
+  pdl_launch();
+}
+
+void swiglu_bf16_launch(float* gu, int64_t gu_stride, int M, int F, __nv_bfloat16* h, int64_t h_stride, bool clear,
+                        cudaStream_t s, bool pdl) {
+  dim3 grid(std::min(64, (F + 255) / 256), M);
+  launch(swiglu_bf16_kernel, grid, dim3(256), 0, s, pdl, gu, gu_stride, F, h, h_stride, (int)clear);
+}
+
 // ---- step advance ----------------------------------------------------------------------------
 __global__ void advance_kernel(int* ids, const int* next_ids, int* positions, int* row_ctx, int R) {
   pdl_wait();

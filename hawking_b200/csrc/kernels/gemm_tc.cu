@@ -1,0 +1,330 @@
+// Tensor-core dequant GEMM (K1, batch >= 16 and prefill): Y[M, N] (+)= X[M, K] . W[N, K]^T with W
+// in GGUF Q4_K, X bf16, fp32 accumulation in TMEM via tcgen05.mma (kind::f16, M=128, N=BN, K=16).
+//
+// One CTA owns a 128-row weight tile and a BN-token tile over a K range (split-K across
+// blockIdx.z, reduced with fp32 atomics). Warp roles:
+//   warp 0      TMA producer of raw Q4_K bytes (header 16 B + 64 B of quants per row per stage)
+//   warp 1      TMA producer of the bf16 activation tile (128-byte swizzle, two 64-wide atoms)
+//   warp 2      TMEM allocation and the single-thread UMMA issuer
+//   warps 4-11  dequantisers: raw smem -> bf16 A tile in the canonical K-major SW128 layout
+//               (bf16x2 FMAs of 128+q nibbles against the sub-block scale/min); warps 4-7 then run
+//               the epilogue (tcgen05.ld 32x32b -> coalesced fp32 stores or atomics)
+// Pipelines: raw (depth 4, TMA -> dequant warps) and A/X (depth 2, dequant warps + TMA -> UMMA,
+// released by tcgen05.commit). All waits are bounded and report through the status word.
+// No TMA multicast is used (the kernel may run in multi-GPU processes).
+//
+// Numerics: the sub-block scale and min products are rounded to bf16 before the dequant FMA and
+// the dequantised weight is bf16, i.e. W4A16 with bf16 weights, fp32 accumulate.
+//
+// Parity: crates/hawking-core/shaders/quant.metal gemm_q4_k_m_batched_v3w(_mma) (simdgroup-MMA batched
+// Q4_K GEMM used by forward_tokens_batch_tcb / multiseq decode, crates/hawking-core/src/model/qwen_dense.rs:7569).
+#include <cudaTypedefs.h>
+
+#include "api.h"
+#include "qformats.cuh"
+#include "sm100.cuh"
+
+namespace hk {
+namespace {
+
+using namespace sm100;
+
+constexpr int BM = 128;        // weight rows per tile (UMMA M)
+constexpr int BK = 128;        // K per stage (half a Q4_K super-block)
+constexpr int DA = 2;          // A/X stages
+constexpr int DR = 4;          // raw weight stages
+constexpr int kThreads = 384;
+constexpr int kDequantWarp0 = 4;
+constexpr int kDequantWarps = 8;
+constexpr uint32_t A_ATOM = BM * 128;       // 16 KB: 128 rows x 64 bf16
+constexpr uint32_t A_STAGE = 2 * A_ATOM;    // 32 KB
+constexpr uint32_t RAW_HDR = BM * 16;       // 2 KB
+constexpr uint32_t RAW_QS = BM * 64;        // 8 KB
+
+template <int BN>
+struct Layout {
+  static constexpr uint32_t X_ATOM = BN * 128;
+  static constexpr uint32_t X_STAGE = 2 * X_ATOM;
+  static constexpr uint32_t off_a = 0;
+  static constexpr uint32_t off_x = off_a + DA * A_STAGE;
+  static constexpr uint32_t off_hdr = off_x + DA * X_STAGE;
+  static constexpr uint32_t off_qs = off_hdr + DR * RAW_HDR;
+  static constexpr uint32_t off_bar = off_qs + DR * RAW_QS;
+  static constexpr uint32_t n_bars = 2 * DR + 2 * DA + 1;
+  static constexpr uint32_t total = off_bar + n_bars * 8 + 16 + 1024;  // + alignment slack
+};
+
+struct TcArgs {
+  int N, K, M;
+  int stages_total, stages_per_split;
+  float* y;
+  int64_t y_stride;
+  int atomic;
+  int* status;
+};
+
+__device__ __forceinline__ uint32_t bf2_bits(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t*>(&v); }
+__device__ __forceinline__ __nv_bfloat162 bits_bf2(uint32_t u) { return *reinterpret_cast<__nv_bfloat162*>(&u); }
+
+// 4 consecutive nibbles (bytes b0..b3 of v, low or high nibble) -> two bf16x2 = q * s + o.
+// (128 + q) is built exactly as a bf16 bit pattern, 128 is subtracted exactly, then one FMA.
+__device__ __forceinline__ uint2 dq4(uint32_t v, int hi, __nv_bfloat162 s2, __nv_bfloat162 o2) {
+  uint32_t t0 = __byte_perm(v, 0, 0x4140);  // [b0, 0, b1, 0]
+  uint32_t t1 = __byte_perm(v, 0, 0x4342);  // [b2, 0, b3, 0]
+  if (hi) { t0 >>= 4; t1 >>= 4; }
+  const uint32_t p0 = (t0 & 0x000F000Fu) | 0x43004300u;  // bf16 (128 + q)
+  const uint32_t p1 = (t1 & 0x000F000Fu) | 0x43004300u;
+  const __nv_bfloat162 c128 = bits_bf2(0x43004300u);
+  uint2 r;
+  r.x = bf2_bits(__hfma2(__hsub2(bits_bf2(p0), c128), s2, o2));
+  r.y = bf2_bits(__hfma2(__hsub2(bits_bf2(p1), c128), s2, o2));
+  return r;
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_gemm_q4k_kernel(const __grid_constant__ CUtensorMap tm_hdr, const __grid_constant__ CUtensorMap tm_qs,
+                       const __grid_constant__ CUtensorMap tm_x, TcArgs a) {
+  using L = Layout<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::off_bar);
+  uint64_t* raw_full = bars;
+  uint64_t* raw_empty = bars + DR;
+  uint64_t* a_full = bars + 2 * DR;
+  uint64_t* a_empty = bars + 2 * DR + DA;
+  uint64_t* acc_full = bars + 2 * DR + 2 * DA;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::n_bars);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * BM, m0 = blockIdx.y * BN;
+  const int s0 = blockIdx.z * a.stages_per_split;
+  const int s1 = min(a.stages_total, s0 + a.stages_per_split);
+  const int nst = max(0, s1 - s0);
+  constexpr uint32_t tmem_cols = BN < 32 ? 32 : BN;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < DR; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], kDequantWarps); }
+    for (int i = 0; i < DA; ++i) { mbar_init(&a_full[i], kDequantWarps + 1); mbar_init(&a_empty[i], 1); }
+    mbar_init(acc_full, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) { prefetch_tmap(&tm_hdr); prefetch_tmap(&tm_qs); prefetch_tmap(&tm_x); }
+  if (warp == 2) tmem_alloc(tmem_slot, tmem_cols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // Weights do not depend on the previous kernel: only the raw producer skips the PDL wait.
+  if (!(warp == 0)) pdl_wait();
+
+  if (nst > 0) {
+    if (warp == 0 && lane == 0) {
+      // ---- raw Q4_K producer ----
+      int issued = 0;
+      for (int i = 0; i < nst; ++i) {
+        const int slot = i % DR;
+        if (!mbar_wait(&raw_empty[slot], ((i / DR) & 1) ^ 1, a.status)) break;
+        const int gs = s0 + i, sb = gs >> 1, h = gs & 1;
+        mbar_arrive_expect_tx(&raw_full[slot], RAW_HDR + RAW_QS);
+        tma_load_2d(smem + L::off_hdr + slot * RAW_HDR, &tm_hdr, sb * 144, n0, &raw_full[slot]);
+        tma_load_2d(smem + L::off_qs + slot * RAW_QS, &tm_qs, sb * 144 + 16 + 64 * h, n0, &raw_full[slot]);
+        ++issued;
+      }
+      // Drain: every issued copy has landed before the CTA may exit.
+      for (int i = max(0, issued - DR); i < issued; ++i) mbar_wait(&raw_full[i % DR], (i / DR) & 1, nullptr, 1u << 22);
+    } else if (warp == 1 && lane == 0) {
+      // ---- activation producer ----
+      int issued = 0;
+      for (int i = 0; i < nst; ++i) {
+        const int slot = i % DA;
+        if (!mbar_wait(&a_empty[slot], ((i / DA) & 1) ^ 1, a.status)) break;
+        const int gs = s0 + i;
+        mbar_arrive_expect_tx(&a_full[slot], L::X_STAGE);
+        uint8_t* xs = smem + L::off_x + slot * L::X_STAGE;
+        tma_load_2d(xs, &tm_x, gs * BK, m0, &a_full[slot]);
+        tma_load_2d(xs + L::X_ATOM, &tm_x, gs * BK + 64, m0, &a_full[slot]);
+        ++issued;
+      }
+      if (issued < nst) {  // error path: give copies in flight time to land before exiting
+        for (int k = 0; k < 2000; ++k) __nanosleep(100);
+      }
+    } else if (warp == 2 && lane == 0) {
+      // ---- UMMA issuer ----
+      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
+      bool ok = true;
+      for (int i = 0; i < nst && ok; ++i) {
+        const int slot = i % DA;
+        ok = mbar_wait(&a_full[slot], (i / DA) & 1, a.status);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t a_base = smem_u32(smem + L::off_a + slot * A_STAGE);
+        const uint32_t x_base = smem_u32(smem + L::off_x + slot * L::X_STAGE);
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t ad = sdesc_k_sw128(a_base + c * A_ATOM + kk * 32);
+            const uint64_t bd = sdesc_k_sw128(x_base + c * L::X_ATOM + kk * 32);
+            umma_f16(tmem, ad, bd, idesc, (i | c | kk) != 0);
+          }
+        umma_commit(&a_empty[slot]);
+      }
+      umma_commit(acc_full);
+    } else if (warp >= kDequantWarp0 && warp < kDequantWarp0 + kDequantWarps) {
+      // ---- dequantisers ----
+      const int t = (warp - kDequantWarp0) * 32 + lane;
+      const int r = t >> 1, c = t & 1;
+      for (int i = 0; i < nst; ++i) {
+        const int rs = i % DR, as = i % DA;
+        const bool ok_raw = __shfl_sync(0xffffffffu, mbar_wait(&raw_full[rs], (i / DR) & 1, a.status), 0);
+        if (!ok_raw) break;
+        const uint4 hdr = *reinterpret_cast<const uint4*>(smem + L::off_hdr + rs * RAW_HDR + r * 16);
+        const uint4 q0 = *reinterpret_cast<const uint4*>(smem + L::off_qs + rs * RAW_QS + r * 64 + c * 32);
+        const uint4 q1 = *reinterpret_cast<const uint4*>(smem + L::off_qs + rs * RAW_QS + r * 64 + c * 32 + 16);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&raw_empty[rs]);
+        const int gs = s0 + i, h = gs & 1;
+        const int j0 = 4 * h + 2 * c;
+        int sc0, mn0, sc1, mn1;
+        q4k_scale_min(j0, hdr.y, hdr.z, hdr.w, sc0, mn0);
+        q4k_scale_min(j0 + 1, hdr.y, hdr.z, hdr.w, sc1, mn1);
+        const float d = __half2float(__ushort_as_half((uint16_t)(hdr.x & 0xFFFF)));
+        const float dm = __half2float(__ushort_as_half((uint16_t)(hdr.x >> 16)));
+        // w = q * (d * sc) - dmin * m, with the two products rounded to bf16
+        const __nv_bfloat162 s2A = __float2bfloat162_rn(d * sc0), s2B = __float2bfloat162_rn(d * sc1);
+        const __nv_bfloat162 o2A = __float2bfloat162_rn(-dm * mn0), o2B = __float2bfloat162_rn(-dm * mn1);
+        const bool ok_a = __shfl_sync(0xffffffffu, mbar_wait(&a_empty[as], ((i / DA) & 1) ^ 1, a.status), 0);
+        if (!ok_a) break;
+        uint8_t* atom = smem + L::off_a + as * A_STAGE + c * A_ATOM;
+        const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) {  // 16-byte chunk = 8 elements = 2 words
+          const uint2 lo0 = dq4(w[2 * ch], 0, s2A, o2A), lo1 = dq4(w[2 * ch + 1], 0, s2A, o2A);
+          const uint2 hi0 = dq4(w[2 * ch], 1, s2B, o2B), hi1 = dq4(w[2 * ch + 1], 1, s2B, o2B);
+          *reinterpret_cast<uint4*>(atom + sw128_offset(r, ch)) = make_uint4(lo0.x, lo0.y, lo1.x, lo1.y);
+          *reinterpret_cast<uint4*>(atom + sw128_offset(r, ch + 4)) = make_uint4(hi0.x, hi0.y, hi1.x, hi1.y);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&a_full[as]);
+      }
+    }
+
+    // ---- epilogue: warps 4..7 (TMEM lane quarter = warp % 4) ----
+    if (warp >= kDequantWarp0 && warp < kDequantWarp0 + 4) {
+      const bool ok = __shfl_sync(0xffffffffu, mbar_wait(acc_full, 0, a.status), 0);
+      tc_fence_after();
+      if (ok) {
+        const int q = warp & 3;
+        const int n = n0 + q * 32 + lane;
+#pragma unroll 1
+        for (int j = 0; j < BN / 8; ++j) {
+          float v[8];
+          tmem_ld_x8(tmem + ((uint32_t)(q * 32) << 16) + j * 8, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const int m = m0 + j * 8 + e;
+            if (m < a.M && n < a.N) {
+              float* dst = a.y + (int64_t)m * a.y_stride + n;
+              if (a.atomic) atomicAdd(dst, v[e]);
+              else *dst = v[e];
+            }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  pdl_launch();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, tmem_cols);
+    tmem_relinquish();
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    HK_CUDA_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+    if (!p || q != cudaDriverEntryPointSuccess) throw std::runtime_error("cuTensorMapEncodeTiled unavailable");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+CUtensorMap make_map_2d(CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
+                        uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                        CUtensorMapSwizzle swz) {
+  if (reinterpret_cast<uintptr_t>(base) % 16) throw std::runtime_error("tma: base not 16-byte aligned");
+  if (row_stride_bytes % 16) throw std::runtime_error("tma: row stride not a multiple of 16 bytes");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = encode_fn()(&m, dt, 2, const_cast<void*>(base), dims, strides, box, es,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+  return m;
+}
+
+template <int BN>
+void launch_bn(const TcGemmArgs& g, cudaStream_t s) {
+  using L = Layout<BN>;
+  const uint64_t rb = (uint64_t)g.w_row_bytes;
+  CUtensorMap tm_hdr = make_map_2d(CU_TENSOR_MAP_DATA_TYPE_UINT8, g.w, rb, g.N, rb, 16, BM, CU_TENSOR_MAP_SWIZZLE_NONE);
+  CUtensorMap tm_qs = make_map_2d(CU_TENSOR_MAP_DATA_TYPE_UINT8, g.w, rb, g.N, rb, 64, BM, CU_TENSOR_MAP_SWIZZLE_NONE);
+  CUtensorMap tm_x = make_map_2d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, g.x, g.K, g.M, (uint64_t)g.x_stride * 2, 64, BN,
+                                 CU_TENSOR_MAP_SWIZZLE_128B);
+  TcArgs a;
+  a.N = g.N;
+  a.K = g.K;
+  a.M = g.M;
+  a.stages_total = g.K / BK;
+  int splits = std::max(1, std::min(g.k_splits, a.stages_total));
+  a.stages_per_split = (a.stages_total + splits - 1) / splits;
+  splits = (a.stages_total + a.stages_per_split - 1) / a.stages_per_split;
+  a.y = g.y;
+  a.y_stride = g.y_stride;
+  a.atomic = (g.atomic || splits > 1) ? 1 : 0;
+  a.status = g.status;
+  static bool attr_set = false;
+  if (!attr_set) {
+    HK_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_q4k_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::total));
+    attr_set = true;
+  }
+  dim3 grid(g.N / BM, (g.M + BN - 1) / BN, splits);
+  launch(tc_gemm_q4k_kernel<BN>, grid, dim3(kThreads), L::total, s, g.pdl, tm_hdr, tm_qs, tm_x, a);
+}
+
+}  // namespace
+
+int tc_gemm_splits(int N, int M, int K, int bn, int sms) {
+  const int tiles = (N / BM) * ((M + bn - 1) / bn);
+  const int stages = K / BK;
+  int splits = (sms + tiles - 1) / tiles;
+  splits = std::min(splits, std::max(1, stages / 4));  // keep >= 4 stages per split
+  return std::max(1, splits);
+}
+
+void tc_gemm_launch(const TcGemmArgs& g, cudaStream_t s) {
+  if (g.fmt != WF_Q4_K) throw std::runtime_error("tc_gemm: only Q4_K weights are supported");
+  if (g.N % BM) throw std::runtime_error("tc_gemm: N must be a multiple of 128");
+  if (g.K % 256) throw std::runtime_error("tc_gemm: K must be a multiple of 256");
+  if (g.k_splits > 1 && !g.atomic && !g.y_zeroed) throw std::runtime_error("tc_gemm: split-K needs a zeroed output");
+  switch (g.bn) {
+    case 32: launch_bn<32>(g, s); break;
+    case 64: launch_bn<64>(g, s); break;
+    case 128: launch_bn<128>(g, s); break;
+    default: throw std::runtime_error("tc_gemm: bn must be 32, 64 or 128");
+  }
+}
+
+}  // namespace hk

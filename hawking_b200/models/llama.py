@@ -266,6 +266,24 @@ class LlamaModel:
         if advance:
             ops.advance(inp.ids, self.next_ids, inp.positions, inp.row_ctx, rows)
 
+    def forward_tokens(self, tokens, seq_id: int = -1, start_pos: int = 0) -> torch.Tensor:
+        """Teacher-forced forward of ``tokens`` for one sequence (positions start_pos..), returning
+        fp32 logits [len(tokens), vocab]. Uses (and extends) the sequence's paged KV."""
+        kv = self.kv
+        n = len(tokens)
+        if not kv.bm.reserve(seq_id, start_pos + n):
+            raise RuntimeError("KV pool exhausted")
+        kv.sync_tables([seq_id])
+        r = kv.row(seq_id)
+        out = torch.empty(n, self.cfg.vocab, device=self.dev)
+        for c0 in range(0, n, self.max_rows):
+            c1 = min(n, c0 + self.max_rows)
+            pos = list(range(start_pos + c0, start_pos + c1))
+            self.inp.upload(tokens[c0:c1], pos, [0] * (c1 - c0), [r] * (c1 - c0), [p + 1 for p in pos])
+            self.forward(c1 - c0, "none")
+            out[c0:c1] = self.logits[: c1 - c0]
+        return out
+
     def xa_view(self, c0, c1, K=None):
         return self._q8_slice(self.xa, c0, c1, K or self.cfg.hidden)
 

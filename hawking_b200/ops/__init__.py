@@ -119,3 +119,23 @@ def sample(logits, temperature, top_k, top_p, rep_penalty, recent, uniforms, out
 def embed(table: QWeight, ids: torch.Tensor, out: torch.Tensor):
     launches.add()
     kernels().embed(table.fmt, table.planes, ids, out, PDL)
+
+
+def tc_gemm(w: QWeight, x: torch.Tensor, y: torch.Tensor, status: torch.Tensor, atomic: bool = False,
+            y_zeroed: bool = False, k_splits: int = 0, bn: int = 0):
+    """y[M, N] (+)= x[M, K] (bf16) @ w[N, K]^T on the tensor cores (Q4_K weights).
+
+    ``k_splits`` 0 picks a split so the grid covers the GPU; split-K accumulates with fp32 atomics,
+    so unless ``atomic`` (residual add) the caller passes a zeroed ``y`` and ``y_zeroed=True``."""
+    M = x.shape[0]
+    if bn == 0:
+        bn = 32 if M <= 32 else (64 if M <= 64 else 128)
+    if k_splits == 0:
+        k_splits = kernels().tc_gemm_splits(w.N, M, w.K, bn, 148) if (atomic or y_zeroed) else 1
+    launches.add()
+    kernels().tc_gemm(w.fmt, w.planes[0], w.N, w.K, x, y, atomic, y_zeroed, k_splits, bn, status, PDL)
+
+
+def swiglu_bf16(gu: torch.Tensor, F: int, h: torch.Tensor, clear: bool = True):
+    launches.add()
+    kernels().swiglu_bf16(gu, F, h, clear, PDL)
