@@ -56,6 +56,102 @@ void swiglu_bf16(const Tensor& gu, int64_t F, const Tensor& h, bool clear, bool 
   hk::swiglu_bf16_launch(gu.data_ptr<float>(), gu.stride(0), (int)gu.size(0), (int)F,
                          reinterpret_cast<__nv_bfloat16*>(h.data_ptr()), h.stride(0), clear, cur_stream(), pdl);
 }
+hk::WPlanes planes_of(const std::vector<Tensor>& ps) {
+  hk::WPlanes w{};
+  const uint8_t** p[4] = {&w.p0, &w.p1, &w.p2, &w.p3};
+  int64_t* rb[4] = {&w.rb0, &w.rb1, &w.rb2, &w.rb3};
+  for (size_t i = 0; i < ps.size() && i < 4; ++i) {
+    TORCH_CHECK(ps[i].is_cuda() && ps[i].stride(-1) == 1, "weight planes must be CUDA rows");
+    *p[i] = reinterpret_cast<const uint8_t*>(ps[i].data_ptr());
+    *rb[i] = ps[i].stride(0) * ps[i].element_size();
+  }
+  return w;
+}
+
+void router_logits(const Tensor& w, const Tensor& xq, const Tensor& xd, const Tensor& logits, bool pdl) {
+  TORCH_CHECK(w.scalar_type() == at::kFloat && w.is_contiguous(), "router weights must be contiguous fp32 [E, K]");
+  const c10::cuda::CUDAGuard g(w.device());
+  hk::router_logits_launch(w.data_ptr<float>(), (int)w.size(0), (int)w.size(1), xq.data_ptr<int8_t>(),
+                           xd.data_ptr<float>(), xq.stride(0), xd.stride(0), logits.data_ptr<float>(),
+                           (int)xq.size(0), cur_stream(), pdl);
+}
+
+void moe_topk(const Tensor& logits, const c10::optional<Tensor>& bias, int64_t k, int64_t scoring,
+              int64_t n_groups, int64_t topk_groups, bool renorm, double scale, const Tensor& ids,
+              const Tensor& weights, bool pdl) {
+  hk::MoeTopkArgs a{};
+  a.logits = logits.data_ptr<float>();
+  a.bias = bias.has_value() ? bias->data_ptr<float>() : nullptr;
+  a.T = (int)logits.size(0);
+  a.E = (int)logits.size(1);
+  a.k = (int)k;
+  a.scoring = (int)scoring;
+  a.n_groups = (int)n_groups;
+  a.topk_groups = (int)topk_groups;
+  a.renorm = renorm;
+  a.scale = (float)scale;
+  a.ids = ids.data_ptr<int>();
+  a.weights = weights.data_ptr<float>();
+  const c10::cuda::CUDAGuard g(logits.device());
+  hk::moe_topk_launch(a, cur_stream(), pdl);
+}
+
+void moe_align(const Tensor& ids, int64_t E, const Tensor& xq, const Tensor& xd, const Tensor& xs,
+               const Tensor& counts, const Tensor& offsets, const Tensor& sorted, const Tensor& gq,
+               const Tensor& gd, const Tensor& gs, bool pdl) {
+  hk::MoeAlignArgs a{};
+  a.ids = ids.data_ptr<int>();
+  a.T = (int)ids.size(0);
+  a.k = (int)ids.size(1);
+  a.E = (int)E;
+  a.K = (int)xq.size(1);
+  a.xq = xq.data_ptr<int8_t>();
+  a.xd = xd.data_ptr<float>();
+  a.xs = xs.data_ptr<float>();
+  a.x_stride_q = xq.stride(0);
+  a.x_stride_s = xd.stride(0);
+  a.counts = counts.data_ptr<int>();
+  a.offsets = offsets.data_ptr<int>();
+  a.sorted = sorted.data_ptr<int>();
+  a.gq = gq.data_ptr<int8_t>();
+  a.gd = gd.data_ptr<float>();
+  a.gs = gs.data_ptr<float>();
+  const c10::cuda::CUDAGuard g(ids.device());
+  hk::moe_align_launch(a, cur_stream(), pdl);
+}
+
+void moe_gemv(int64_t fmt, int64_t epi, const std::vector<Tensor>& w0, const std::vector<Tensor>& w1, int64_t N,
+              int64_t K, int64_t E, int64_t k, const Tensor& counts, const Tensor& offsets, const Tensor& sorted,
+              const Tensor& xq, const Tensor& xd, const Tensor& xs, const c10::optional<Tensor>& oq,
+              const c10::optional<Tensor>& od, const c10::optional<Tensor>& os, const c10::optional<Tensor>& y,
+              const c10::optional<Tensor>& route_w, bool pdl) {
+  hk::MoeGemvArgs a{};
+  a.w0 = planes_of(w0);
+  if (!w1.empty()) a.w1 = planes_of(w1);
+  a.N = (int)N;
+  a.K = (int)K;
+  a.E = (int)E;
+  a.k = (int)k;
+  a.counts = counts.data_ptr<int>();
+  a.offsets = offsets.data_ptr<int>();
+  a.sorted = sorted.data_ptr<int>();
+  a.xq = xq.data_ptr<int8_t>();
+  a.xd = xd.data_ptr<float>();
+  a.xs = xs.data_ptr<float>();
+  if (epi == 0) {
+    TORCH_CHECK(oq.has_value() && od.has_value() && os.has_value() && !w1.empty(), "moe_gemv swiglu: outputs");
+    a.oq = oq->data_ptr<int8_t>();
+    a.od = od->data_ptr<float>();
+    a.os = os->data_ptr<float>();
+  } else {
+    TORCH_CHECK(y.has_value() && route_w.has_value(), "moe_gemv down: y and route weights required");
+    a.y = y->data_ptr<float>();
+    a.y_stride = y->stride(0);
+    a.route_w = route_w->data_ptr<float>();
+  }
+  const c10::cuda::CUDAGuard g(xq.device());
+  hk::moe_gemv_launch((int)fmt, (int)epi, a, cur_stream(), pdl);
+}
 }  // namespace
 
 namespace hk {
@@ -65,6 +161,19 @@ void register_more_kernels(py::module_& m) {
         py::arg("atomic"), py::arg("y_zeroed"), py::arg("k_splits"), py::arg("bn"), py::arg("status"),
         py::arg("pdl") = false);
   m.def("tc_gemm_splits", &hk::tc_gemm_splits);
+  m.def("router_logits", &router_logits, py::arg("w"), py::arg("xq"), py::arg("xd"), py::arg("logits"),
+        py::arg("pdl") = false);
+  m.def("moe_topk", &moe_topk, py::arg("logits"), py::arg("bias"), py::arg("k"), py::arg("scoring"),
+        py::arg("n_groups"), py::arg("topk_groups"), py::arg("renorm"), py::arg("scale"), py::arg("ids"),
+        py::arg("weights"), py::arg("pdl") = false);
+  m.def("moe_align", &moe_align, py::arg("ids"), py::arg("E"), py::arg("xq"), py::arg("xd"), py::arg("xs"),
+        py::arg("counts"), py::arg("offsets"), py::arg("sorted"), py::arg("gq"), py::arg("gd"), py::arg("gs"),
+        py::arg("pdl") = false);
+  m.def("moe_gemv", &moe_gemv, py::arg("fmt"), py::arg("epi"), py::arg("w0"), py::arg("w1"), py::arg("N"),
+        py::arg("K"), py::arg("E"), py::arg("k"), py::arg("counts"), py::arg("offsets"), py::arg("sorted"),
+        py::arg("xq"), py::arg("xd"), py::arg("xs"), py::arg("oq") = py::none(), py::arg("od") = py::none(),
+        py::arg("os") = py::none(), py::arg("y") = py::none(), py::arg("route_w") = py::none(),
+        py::arg("pdl") = false);
   m.def("swiglu_bf16", &swiglu_bf16, py::arg("gu"), py::arg("F"), py::arg("h"), py::arg("clear") = true,
         py::arg("pdl") = false);
 }

@@ -151,6 +151,57 @@ void tc_gemm_launch(const TcGemmArgs& g, cudaStream_t s);
 void swiglu_bf16_launch(float* gu, int64_t gu_stride, int M, int F, __nv_bfloat16* h, int64_t h_stride,
                         bool clear, cudaStream_t s, bool pdl);
 
+// ---- mixture of experts (moe.cu) ----
+void router_logits_launch(const float* w, int E, int K, const int8_t* xq, const float* xd, int64_t xs_q,
+                          int64_t xs_d, float* logits, int T, cudaStream_t s, bool pdl);
+
+struct MoeTopkArgs {
+  const float* logits;   // [T, E]
+  const float* bias;     // optional [E] selection bias (sigmoid scoring)
+  int T, E, k;
+  int scoring;           // 0 softmax, 1 sigmoid
+  int n_groups, topk_groups;
+  int renorm;
+  float scale;           // routed scaling factor
+  int* ids;              // [T, k]
+  float* weights;        // [T, k]
+};
+void moe_topk_launch(const MoeTopkArgs& a, cudaStream_t s, bool pdl);
+
+struct MoeAlignArgs {
+  const int* ids;        // [T, k]
+  int T, k, E, K;
+  const int8_t* xq;      // token activations (q8) [T, K]
+  const float* xd;
+  const float* xs;
+  int64_t x_stride_q, x_stride_s;
+  int* counts;           // [E]
+  int* offsets;          // [E]
+  int* sorted;           // [T*k] pair ids (t*k + j) grouped by expert
+  int8_t* gq;            // gathered activations [T*k, K] (sorted order)
+  float* gd;
+  float* gs;
+};
+void moe_align_launch(const MoeAlignArgs& a, cudaStream_t s, bool pdl);
+
+struct MoeGemvArgs {
+  WPlanes w0, w1;        // stacked expert weights [E * N, K] (w1: up projection for epi 0)
+  int N, K, E, k;
+  const int* counts;
+  const int* offsets;
+  const int* sorted;
+  const int8_t* xq;      // inputs in sorted order [T*k, K]
+  const float* xd;
+  const float* xs;
+  int8_t* oq;            // epi 0: SwiGLU output q8 in sorted order [T*k, N]
+  float* od;
+  float* os;
+  float* y;              // epi 1: residual [T, y_stride] (atomic add of route_w * y)
+  int64_t y_stride;
+  const float* route_w;  // [T*k]
+};
+void moe_gemv_launch(int fmt, int epi, const MoeGemvArgs& a, cudaStream_t s, bool pdl);
+
 // ---- quantisers (quantize.cu) ----
 // n elements (rows * cols, cols a multiple of the block) -> planes p0..p3 of format fmt.
 void quantize_launch(int fmt, const float* x, int64_t n, void* p0, void* p1, void* p2, void* p3, cudaStream_t s);

@@ -41,7 +41,8 @@ __global__ void quantize_q4k_kernel(const float* __restrict__ x, int64_t nblocks
     mn[j] = (uint8_t)min(max(dmin != 0.f ? __float2int_rn(mins[j] / dmin) : 0, 0), 63);
   }
   const uint16_t dh = f2h_bits(d), mh = f2h_bits(dmin);
-  o[0] = dh & 0xFF; o[1] = dh >> 8; o[2] = mh & 0xFF; o[3] = mh >> 8;
+  reinterpret_cast<uint16_t*>(o)[0] = dh;  // 16-bit stores (o is 4-byte aligned: 144-byte blocks)
+  reinterpret_cast<uint16_t*>(o)[1] = mh;
   for (int j = 0; j < 4; ++j) {
     o[4 + j] = (uint8_t)((sc[j] & 63) | ((sc[j + 4] >> 4) << 6));
     o[8 + j] = (uint8_t)((mn[j] & 63) | ((mn[j + 4] >> 4) << 6));

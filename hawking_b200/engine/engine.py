@@ -129,14 +129,25 @@ class Engine:
         for c0 in range(0, n, R):
             c1 = min(n, c0 + R)
             self.stats.h2d_bytes += m.inp.upload(ids[c0:c1], pos[c0:c1], slots[c0:c1], rseq[c0:c1], rctx[c0:c1])
+            rows_here = [(it, r - c0) for it, r in sample_rows if c0 <= r < c1]
             if self.use_graphs and decode_only and c1 - c0 == n:
                 m.graph_forward(c1 - c0, mode)
                 self.stats.graph_steps += 1
+                picks = [(it, r) for it, r in rows_here]
             else:
-                m.forward(c1 - c0, mode)
-            rows_here = [(it, r - c0) for it, r in sample_rows if c0 <= r < c1]
+                k = len(rows_here)
+                if k == 0:
+                    m.forward(c1 - c0, "none", n_logits=-1)
+                else:
+                    if k == c1 - c0:
+                        m.forward(c1 - c0, mode)
+                    else:
+                        m.logit_rows[:k].copy_(torch.tensor([r for _, r in rows_here], dtype=torch.int32),
+                                               non_blocking=True)
+                        m.forward(c1 - c0, mode, n_logits=k)
+                picks = [(it, j) for j, (it, _) in enumerate(rows_here)] if 0 < k < c1 - c0 else rows_here
             if rows_here:
-                sampled.extend(self._sample(rows_here, greedy))
+                sampled.extend(self._sample(picks, greedy))
         events = self.sched.commit(plan, sampled)
         now = time.perf_counter()
         out = []

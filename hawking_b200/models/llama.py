@@ -45,6 +45,13 @@ class LayerWeights:
     q_norm: Optional[torch.Tensor] = None
     k_norm: Optional[torch.Tensor] = None
     moe: Optional[object] = None  # MoE FFN module (models/moe.py)
+    w_gu: Optional[QWeight] = None  # fused [gate | up] rows (w_gate / w_up are views of it)
+
+    def fuse_gate_up(self):
+        if self.w_gate is not None and self.w_gate.fmt == self.w_up.fmt and self.w_gu is None:
+            F = self.w_gate.N
+            self.w_gu = cat_rows([self.w_gate, self.w_up])
+            self.w_gate, self.w_up = self.w_gu.rows(0, F), self.w_gu.rows(F, F)
 
 
 @dataclass
@@ -59,7 +66,8 @@ class LlamaWeights:
     def nbytes(self) -> int:
         n = self.embed.nbytes + self.lm_head.nbytes
         for l in self.layers:
-            for w in l.wqkv + [l.wo, l.w_gate, l.w_up, l.w_down]:
+            ws = l.wqkv + [l.wo, l.w_down] + ([l.w_gu] if l.w_gu is not None else [l.w_gate, l.w_up])
+            for w in ws:
                 if w is not None:
                     n += w.nbytes
             if l.moe is not None:
@@ -107,6 +115,7 @@ def load_llama_weights(m: GgufModel, cfg: ModelConfig, device) -> LlamaWeights:
             lw.moe = MoEFFN.from_gguf(m, cfg, l, device, qw, vec)
         else:
             lw.w_gate, lw.w_up, lw.w_down = qw(p + "ffn_gate.weight"), qw(p + "ffn_up.weight"), qw(p + "ffn_down.weight")
+            lw.fuse_gate_up()
         layers.append(lw)
     embed = QWeight.from_raw(raw("token_embd.weight"), m.tensors["token_embd.weight"].type, cfg.vocab, cfg.hidden)
     head = qw("output.weight") if m.has("output.weight") else (
@@ -142,7 +151,9 @@ def random_llama_weights(cfg: ModelConfig, device, seed: int = 0, std: float = 0
             from .moe import MoEFFN
             lw.moe = MoEFFN.random(cfg, device, g, std)
         else:
-            lw.w_gate, lw.w_up, lw.w_down = W(cfg.ffn, H), W(cfg.ffn, H), W(H, cfg.ffn)
+            gu = W(2 * cfg.ffn, H)
+            lw.w_gu, lw.w_gate, lw.w_up = gu, gu.rows(0, cfg.ffn), gu.rows(cfg.ffn, cfg.ffn)
+            lw.w_down = W(H, cfg.ffn)
         layers.append(lw)
     embed = W(cfg.vocab, H, efmt)
     head = embed if cfg.tie_embeddings else W(cfg.vocab, H)
@@ -183,6 +194,7 @@ class LlamaModel:
                  max_splits: int = 64):
         self.cfg, self.w, self.kv, self.dev = cfg, weights, kv, torch.device(device)
         self.max_rows = max_rows
+        self.max_splits = max_splits
         H, hd, nh, nkv = cfg.hidden, cfg.head_dim, cfg.n_heads, cfg.n_kv_heads
         F = max([cfg.ffn, cfg.expert_ffn, cfg.shared_ffn, 32])
         qkv_n = (nh + 2 * nkv) * hd
@@ -194,10 +206,17 @@ class LlamaModel:
         self.hq = Q8Act(R, F, self.dev)
         self.qkv = torch.zeros(R, qkv_n, device=self.dev)
         self.q = torch.zeros(R, nh, hd, device=self.dev)
-        self.max_splits = max_splits
-        self.part_o = torch.zeros(R * nh * max_splits * hd, device=self.dev)
-        self.part_lse = torch.zeros(R * nh * max_splits, device=self.dev)
+        cap = max(r * self.num_splits(r) for r in range(1, R + 1))
+        self.part_o = torch.zeros(cap * nh * hd, device=self.dev)
+        self.part_lse = torch.zeros(cap * nh, device=self.dev)
         self.logits = torch.zeros(R, cfg.vocab, device=self.dev)
+        # tensor-core path buffers (bf16 activations; fp32 outputs kept zeroed between uses)
+        self.xb = torch.zeros(R, H, dtype=torch.bfloat16, device=self.dev)
+        self.attb = torch.zeros(R, nh * hd, dtype=torch.bfloat16, device=self.dev)
+        self.hb = torch.zeros(R, F, dtype=torch.bfloat16, device=self.dev)
+        self.gu = torch.zeros(R, 2 * F, device=self.dev)
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.dev)
+        self.logit_rows = torch.zeros(R, dtype=torch.int32, device=self.dev)
         self.next_ids = torch.zeros(R, dtype=torch.int32, device=self.dev)
         self.rope = ops.rope_table(cfg.max_ctx, cfg.rope_dim, cfg.rope_theta, weights.rope_freqs, self.dev)
         self.scale = 1.0 / math.sqrt(hd)
@@ -219,52 +238,115 @@ class LlamaModel:
         for c0 in range(0, rows, GEMV_COLS):
             fn(c0, min(rows, c0 + GEMV_COLS))
 
-    def forward(self, rows: int, sample: str = "greedy", advance: bool = False):
+    def use_tensor_cores(self, rows: int) -> bool:
+        l0 = self.w.layers[0]
+        return rows > GEMV_COLS and all(w.fmt == GgmlType.Q4_K for w in l0.wqkv + [l0.wo]) and \
+            l0.moe is None and l0.w_gu is not None and l0.w_gu.fmt == GgmlType.Q4_K and \
+            l0.w_down.fmt == GgmlType.Q4_K
+
+    def forward(self, rows: int, sample: str = "greedy", advance: bool = False, n_logits: int = 0):
         """Forward ``rows`` rows from the static inputs; leaves logits and (greedy) next_ids.
-        ``advance`` feeds next_ids back as the next step's inputs on the device (back-to-back
-        decode without a host round trip)."""
+
+        ``n_logits`` > 0 computes logits only for the rows listed in ``self.logit_rows[:n_logits]``
+        (their logits land in ``self.logits[:n_logits]``). ``advance`` feeds next_ids back as the
+        next step's inputs on the device (back-to-back decode without a host round trip)."""
         cfg, w, kv = self.cfg, self.w, self.kv
         nh, nkv, hd = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
         inp = self.inp
         x = self.x[:rows]
+        tc = self.use_tensor_cores(rows)
         ops.embed(w.embed, inp.ids[:rows], x)
         splits = self.num_splits(rows)
         for l, lw in enumerate(w.layers):
-            ops.rmsnorm_q8(x, lw.attn_norm, cfg.eps, self.xa.view(rows))
-
-            def qkv_fn(c0, c1):
-                xa = self.xa_view(c0, c1)
-                off = 0
-                for wt in lw.wqkv:
-                    ops.gemv(wt, xa, self.qkv[c0:c1, off:off + wt.N])
-                    off += wt.N
-            self._gemv_cols(qkv_fn, rows)
-            ops.rope_append(self.qkv[:rows], inp.positions[:rows], None, self.rope, cfg.rope_dim,
-                            cfg.rope_style, self.q[:rows], kv.k[l], kv.v[l], nh, nkv, hd, kv.block_size,
-                            bias=lw.qkv_bias, q_norm=lw.q_norm, k_norm=lw.k_norm, eps=cfg.eps,
-                            block_tables=kv.block_tables, row_seq=inp.row_seq[:rows])
-            ops.attention_decode(self.q[:rows], kv.k[l], kv.v[l], kv.block_tables, inp.row_seq[:rows],
-                                 inp.row_ctx[:rows], self.scale, splits, self.part_o, self.part_lse,
-                                 out_q8=self.att.view(rows))
-            self._gemv_cols(lambda c0, c1: ops.gemv(lw.wo, self._q8_slice(self.att, c0, c1), x[c0:c1],
-                                                    residual=True), rows)
-            ops.rmsnorm_q8(x, lw.ffn_norm, cfg.eps, self.xa.view(rows))
-            if lw.moe is not None:
-                lw.moe.forward(self, rows)
+            if tc:
+                self._attention_block_tc(l, lw, rows, splits)
+                self._ffn_block_tc(lw, rows)
             else:
-                self._gemv_cols(lambda c0, c1: ops.gemv_swiglu(lw.w_gate, lw.w_up, self.xa_view(c0, c1),
-                                                               self._q8_slice(self.hq, c0, c1)), rows)
-                self._gemv_cols(lambda c0, c1: ops.gemv(lw.w_down, self._q8_slice(self.hq, c0, c1, lw.w_down.K),
-                                                        x[c0:c1], residual=True), rows)
-        ops.rmsnorm_q8(x, w.out_norm, cfg.eps, self.xa.view(rows))
-        self._gemv_cols(lambda c0, c1: ops.gemv(w.lm_head, self.xa_view(c0, c1), self.logits[c0:c1]), rows)
+                self._attention_block_gemv(l, lw, rows, splits)
+                ops.rmsnorm_q8(x, lw.ffn_norm, cfg.eps, self.xa.view(rows))
+                if lw.moe is not None:
+                    lw.moe.forward(self, rows)
+                else:
+                    self._gemv_cols(lambda c0, c1: ops.gemv_swiglu(lw.w_gate, lw.w_up, self.xa_view(c0, c1),
+                                                                   self._q8_slice(self.hq, c0, c1)), rows)
+                    self._gemv_cols(lambda c0, c1: ops.gemv(lw.w_down,
+                                                            self._q8_slice(self.hq, c0, c1, lw.w_down.K),
+                                                            x[c0:c1], residual=True), rows)
+        if n_logits < 0:  # no row of this chunk is sampled
+            if advance:
+                ops.advance(inp.ids, self.next_ids, inp.positions, inp.row_ctx, rows)
+            return
+        nl = n_logits or rows
+        if tc and w.lm_head.fmt == GgmlType.Q4_K:
+            ops.rmsnorm(x, w.out_norm, cfg.eps, yb=self.xb[:rows])
+            src = self.xb[:rows]
+            if n_logits:
+                src = self.xb.index_select(0, self.logit_rows[:nl].long())
+            self.logits[:nl].zero_()
+            ops.tc_gemm(w.lm_head, src, self.logits[:nl], self.status, y_zeroed=True)
+        else:
+            ops.rmsnorm_q8(x, w.out_norm, cfg.eps, self.xa.view(rows))
+            xa = self.xa
+            if n_logits:
+                idx = self.logit_rows[:nl].long()
+                xa = Q8Act.__new__(Q8Act)
+                xa.K, xa.q, xa.d, xa.s = self.xa.K, self.xa.q.index_select(0, idx), \
+                    self.xa.d.index_select(0, idx), self.xa.s.index_select(0, idx)
+            self._gemv_cols(lambda c0, c1: ops.gemv(w.lm_head, self._q8_slice(xa, c0, c1, cfg.hidden),
+                                                    self.logits[c0:c1]), nl)
         if sample == "greedy":
-            ops.argmax(self.logits[:rows], self.next_ids[:rows])
+            ops.argmax(self.logits[:nl], self.next_ids[:nl])
         elif sample == "sample":
-            ops.sample(self.logits[:rows], self.temperature[:rows], self.top_k[:rows], self.top_p[:rows],
-                       self.rep_penalty[:rows], None, self.uniforms[:rows], self.next_ids[:rows])
+            ops.sample(self.logits[:nl], self.temperature[:nl], self.top_k[:nl], self.top_p[:nl],
+                       self.rep_penalty[:nl], None, self.uniforms[:nl], self.next_ids[:nl])
         if advance:
             ops.advance(inp.ids, self.next_ids, inp.positions, inp.row_ctx, rows)
+
+    def _rope_attention(self, l, lw, rows, splits, out_q8=None, out_bf16=None):
+        cfg, kv, inp = self.cfg, self.kv, self.inp
+        ops.rope_append(self.qkv[:rows], inp.positions[:rows], None, self.rope, cfg.rope_dim,
+                        cfg.rope_style, self.q[:rows], kv.k[l], kv.v[l], cfg.n_heads, cfg.n_kv_heads,
+                        cfg.head_dim, kv.block_size, bias=lw.qkv_bias, q_norm=lw.q_norm, k_norm=lw.k_norm,
+                        eps=cfg.eps, block_tables=kv.block_tables, row_seq=inp.row_seq[:rows])
+        ops.attention_decode(self.q[:rows], kv.k[l], kv.v[l], kv.block_tables, inp.row_seq[:rows],
+                             inp.row_ctx[:rows], self.scale, splits, self.part_o, self.part_lse,
+                             out_q8=out_q8, out_bf16=out_bf16)
+
+    def _attention_block_gemv(self, l, lw, rows, splits):
+        x = self.x[:rows]
+        ops.rmsnorm_q8(x, lw.attn_norm, self.cfg.eps, self.xa.view(rows))
+
+        def qkv_fn(c0, c1):
+            xa = self.xa_view(c0, c1)
+            off = 0
+            for wt in lw.wqkv:
+                ops.gemv(wt, xa, self.qkv[c0:c1, off:off + wt.N])
+                off += wt.N
+        self._gemv_cols(qkv_fn, rows)
+        self._rope_attention(l, lw, rows, splits, out_q8=self.att.view(rows))
+        self._gemv_cols(lambda c0, c1: ops.gemv(lw.wo, self._q8_slice(self.att, c0, c1), x[c0:c1],
+                                                residual=True), rows)
+
+    def _attention_block_tc(self, l, lw, rows, splits):
+        x = self.x[:rows]
+        ops.rmsnorm(x, lw.attn_norm, self.cfg.eps, yb=self.xb[:rows])
+        qkv = self.qkv[:rows]
+        qkv.zero_()
+        off = 0
+        for wt in lw.wqkv:
+            ops.tc_gemm(wt, self.xb[:rows], qkv[:, off:off + wt.N], self.status, y_zeroed=True)
+            off += wt.N
+        self._rope_attention(l, lw, rows, splits, out_bf16=self.attb[:rows])
+        ops.tc_gemm(lw.wo, self.attb[:rows], x, self.status, atomic=True)
+
+    def _ffn_block_tc(self, lw, rows):
+        x = self.x[:rows]
+        F = lw.w_down.K
+        ops.rmsnorm(x, lw.ffn_norm, self.cfg.eps, yb=self.xb[:rows])
+        gu = self.gu[:rows, : 2 * F]
+        ops.tc_gemm(lw.w_gu, self.xb[:rows], gu, self.status, y_zeroed=True)
+        ops.swiglu_bf16(gu, F, self.hb[:rows, :F], clear=True)
+        ops.tc_gemm(lw.w_down, self.hb[:rows, :F], x, self.status, atomic=True)
 
     def forward_tokens(self, tokens, seq_id: int = -1, start_pos: int = 0) -> torch.Tensor:
         """Teacher-forced forward of ``tokens`` for one sequence (positions start_pos..), returning
@@ -280,7 +362,7 @@ class LlamaModel:
             c1 = min(n, c0 + self.max_rows)
             pos = list(range(start_pos + c0, start_pos + c1))
             self.inp.upload(tokens[c0:c1], pos, [0] * (c1 - c0), [r] * (c1 - c0), [p + 1 for p in pos])
-            self.forward(c1 - c0, "none")
+            self.forward(c1 - c0, "none", n_logits=0)
             out[c0:c1] = self.logits[: c1 - c0]
         return out
 

@@ -99,11 +99,11 @@ def advance(ids, next_ids, positions, row_ctx, rows: int):
 
 
 def attention_decode(q, k_cache, v_cache, block_tables, row_seq, row_ctx, scale, num_splits, part_o, part_lse,
-                     out=None, out_q8: Optional[Q8Act] = None, sinks=None):
+                     out=None, out_q8: Optional[Q8Act] = None, sinks=None, out_bf16=None):
     launches.add(2)
     kernels().attention_decode(q, k_cache, v_cache, block_tables, row_seq, row_ctx, scale, num_splits, part_o,
                                part_lse, out, out_q8.q if out_q8 else None, out_q8.d if out_q8 else None,
-                               out_q8.s if out_q8 else None, sinks, PDL)
+                               out_q8.s if out_q8 else None, sinks, out_bf16, PDL)
 
 
 def argmax(logits: torch.Tensor, out: torch.Tensor):
@@ -130,7 +130,7 @@ def tc_gemm(w: QWeight, x: torch.Tensor, y: torch.Tensor, status: torch.Tensor, 
     M = x.shape[0]
     if bn == 0:
         bn = 32 if M <= 32 else (64 if M <= 64 else 128)
-    if k_splits == 0:
+    if k_splits == 0 or k_splits is None:
         k_splits = kernels().tc_gemm_splits(w.N, M, w.K, bn, 148) if (atomic or y_zeroed) else 1
     launches.add()
     kernels().tc_gemm(w.fmt, w.planes[0], w.N, w.K, x, y, atomic, y_zeroed, k_splits, bn, status, PDL)
