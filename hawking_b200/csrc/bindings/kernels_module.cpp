@@ -37,24 +37,42 @@ hk::WPlanes planes(const std::vector<Tensor>& ps) {
 }
 
 void gemv(int64_t fmt, int64_t epi, const std::vector<Tensor>& w0, const std::vector<Tensor>& w1, int64_t N,
-          int64_t K, const Tensor& xq, const Tensor& xd, const Tensor& xs, const optional<Tensor>& y,
-          const optional<Tensor>& bias, const optional<Tensor>& oq, const optional<Tensor>& od,
-          const optional<Tensor>& os, bool pdl) {
-  check_cuda(xq, "xq");
-  TORCH_CHECK(xq.scalar_type() == at::kChar && xd.scalar_type() == at::kFloat && xs.scalar_type() == at::kFloat,
-              "gemv: activations must be int8 q / fp32 d / fp32 s");
-  TORCH_CHECK(xq.dim() == 2 && xq.size(1) >= K && xq.stride(1) == 1, "gemv: xq must be [nb, K]");
-  const int nb = (int)xq.size(0);
+          int64_t K, const optional<Tensor>& xq_, const optional<Tensor>& xd_, const optional<Tensor>& xs_,
+          const optional<Tensor>& y, const optional<Tensor>& bias, const optional<Tensor>& oq,
+          const optional<Tensor>& od, const optional<Tensor>& os, const optional<Tensor>& x_f32,
+          const optional<Tensor>& norm_w, double eps, bool pdl) {
   hk::GemvArgs a{};
+  int nb;
+  if (x_f32.has_value()) {
+    check_cuda(*x_f32, "x_f32");
+    TORCH_CHECK(x_f32->scalar_type() == at::kFloat && x_f32->stride(-1) == 1 && x_f32->size(1) >= K,
+                "gemv: x_f32 must be fp32 [nb, K]");
+    nb = (int)x_f32->size(0);
+    a.x_f32 = x_f32->data_ptr<float>();
+    a.x_f32_stride = x_f32->stride(0);
+    a.norm_w = optr<float>(norm_w);
+    a.eps = (float)eps;
+    a.norm = eps >= 0.0 ? 1 : 0;
+  } else {
+    TORCH_CHECK(xq_.has_value() && xd_.has_value() && xs_.has_value(), "gemv: q8 activations required");
+    const Tensor& xq = *xq_;
+    const Tensor& xd = *xd_;
+    const Tensor& xs = *xs_;
+    check_cuda(xq, "xq");
+    TORCH_CHECK(xq.scalar_type() == at::kChar && xd.scalar_type() == at::kFloat && xs.scalar_type() == at::kFloat,
+                "gemv: activations must be int8 q / fp32 d / fp32 s");
+    TORCH_CHECK(xq.dim() == 2 && xq.size(1) >= K && xq.stride(1) == 1, "gemv: xq must be [nb, K]");
+    nb = (int)xq.size(0);
+    a.xq = ptr<int8_t>(xq);
+    a.xd = ptr<float>(xd);
+    a.xs = ptr<float>(xs);
+    a.x_stride_q = xq.stride(0);
+    a.x_stride_s = xd.stride(0);
+  }
   a.w0 = planes(w0);
   if (!w1.empty()) a.w1 = planes(w1);
   a.N = (int)N;
   a.K = (int)K;
-  a.xq = ptr<int8_t>(xq);
-  a.xd = ptr<float>(xd);
-  a.xs = ptr<float>(xs);
-  a.x_stride_q = xq.stride(0);
-  a.x_stride_s = xd.stride(0);
   if (y.has_value()) {
     TORCH_CHECK(y->scalar_type() == at::kFloat && y->stride(-1) == 1 && y->size(0) >= nb && y->size(-1) >= N,
                 "gemv: y must be fp32 [nb, >=N]");
@@ -73,7 +91,7 @@ void gemv(int64_t fmt, int64_t epi, const std::vector<Tensor>& w0, const std::ve
   } else {
     TORCH_CHECK(a.y, "gemv: output y required");
   }
-  const c10::cuda::CUDAGuard g(xq.device());
+  const c10::cuda::CUDAGuard g(w0[0].device());
   hk::gemv_launch((int)fmt, (int)epi, a, nb, cur_stream(), pdl);
 }
 
@@ -138,7 +156,8 @@ void attention_decode(const Tensor& q, const Tensor& k_cache, const Tensor& v_ca
                       const Tensor& row_seq, const Tensor& row_ctx, double scale, int64_t num_splits,
                       const Tensor& part_o, const Tensor& part_lse, const optional<Tensor>& out,
                       const optional<Tensor>& oq, const optional<Tensor>& od, const optional<Tensor>& os,
-                      const optional<Tensor>& sinks, const optional<Tensor>& out_bf16, bool pdl) {
+                      const optional<Tensor>& sinks, const optional<Tensor>& out_bf16,
+                      const optional<Tensor>& counters, bool pdl) {
   check_cuda(q, "q");
   TORCH_CHECK(q.dim() == 3 && q.scalar_type() == at::kFloat, "q must be fp32 [R, nh, hd]");
   TORCH_CHECK(k_cache.dim() == 4 && k_cache.scalar_type() == at::kBFloat16, "k_cache must be bf16 [blocks, nkv, bs, hd]");
@@ -170,6 +189,8 @@ void attention_decode(const Tensor& q, const Tensor& k_cache, const Tensor& v_ca
   a.os = optr<float>(os);
   a.sinks = optr<float>(sinks);
   a.out_bf16 = optr<__nv_bfloat16>(out_bf16);
+  a.counters = optr<int>(counters);
+  TORCH_CHECK(!counters.has_value() || counters->numel() >= (int64_t)R * a.nkv, "attention: counters too small");
   const c10::cuda::CUDAGuard g(q.device());
   hk::attention_decode_launch(a, cur_stream(), pdl);
 }
@@ -217,7 +238,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "hawking_b200 sm_100a kernels";
   m.def("gemv", &gemv, py::arg("fmt"), py::arg("epi"), py::arg("w0"), py::arg("w1"), py::arg("N"), py::arg("K"),
         py::arg("xq"), py::arg("xd"), py::arg("xs"), py::arg("y") = py::none(), py::arg("bias") = py::none(),
-        py::arg("oq") = py::none(), py::arg("od") = py::none(), py::arg("os") = py::none(), py::arg("pdl") = false);
+        py::arg("oq") = py::none(), py::arg("od") = py::none(), py::arg("os") = py::none(),
+        py::arg("x_f32") = py::none(), py::arg("norm_w") = py::none(), py::arg("eps") = -1.0,
+        py::arg("pdl") = false);
   m.def("rmsnorm_q8", &rmsnorm_q8, py::arg("x"), py::arg("w"), py::arg("eps"), py::arg("norm"), py::arg("xq"),
         py::arg("xd"), py::arg("xs"), py::arg("y") = py::none(), py::arg("pdl") = false);
   m.def("rmsnorm", &rmsnorm, py::arg("x"), py::arg("w"), py::arg("eps"), py::arg("yf") = py::none(),
@@ -238,7 +261,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("block_tables"), py::arg("row_seq"), py::arg("row_ctx"), py::arg("scale"), py::arg("num_splits"),
         py::arg("part_o"), py::arg("part_lse"), py::arg("out") = py::none(), py::arg("oq") = py::none(),
         py::arg("od") = py::none(), py::arg("os") = py::none(), py::arg("sinks") = py::none(),
-        py::arg("out_bf16") = py::none(), py::arg("pdl") = false);
+        py::arg("out_bf16") = py::none(), py::arg("counters") = py::none(), py::arg("pdl") = false);
   m.def("argmax", &argmax, py::arg("logits"), py::arg("out"), py::arg("pdl") = false);
   m.def("sample", &sample, py::arg("logits"), py::arg("temperature"), py::arg("top_k"), py::arg("top_p"),
         py::arg("rep_penalty"), py::arg("recent"), py::arg("uniforms"), py::arg("out"), py::arg("pdl") = false);

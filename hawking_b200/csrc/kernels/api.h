@@ -28,6 +28,7 @@ struct XQ {
 // ---- small-batch dequant GEMV (gemv.cu) ----
 
 enum GemvEpilogue : int { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU_Q8 = 2 };
+enum GemvInput : int { XIN_Q8 = 0, XIN_NORM = 1 };
 
 struct GemvArgs {
   WPlanes w0, w1;          // w1 used by the SwiGLU pair epilogue (up projection)
@@ -43,6 +44,13 @@ struct GemvArgs {
   float* od;
   float* os;
   int64_t o_stride_q, o_stride_s;
+  // Fused-norm input (used instead of xq/xd/xs when x_f32 != nullptr): fp32 rows, optional
+  // RMSNorm with weight norm_w, quantised to q8 blocks inside each CTA.
+  const float* x_f32;
+  int64_t x_f32_stride;
+  const float* norm_w;
+  float eps;
+  int norm;
 };
 
 void gemv_launch(int fmt, int epi, const GemvArgs& a, int nb, cudaStream_t s, bool pdl);
@@ -97,6 +105,7 @@ struct AttnDecodeArgs {
   float* os;
   const float* sinks;          // optional per-head attention sink logits [nh]
   __nv_bfloat16* out_bf16;     // optional [R, nh*hd] bf16 output (tensor-core GEMM path)
+  int* counters;               // [R * nkv] zero-initialised split counters (scratch; reset after use)
 };
 void attention_decode_launch(const AttnDecodeArgs& a, cudaStream_t s, bool pdl);
 

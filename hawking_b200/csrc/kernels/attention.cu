@@ -4,9 +4,10 @@
 // heads that share it, and a contiguous token range of one query row; its 4 warps interleave over
 // tiles of T = 32/G tokens. Each lane holds hd/32 contiguous dims of the G query vectors, so a
 // tile's G*T partial dot products are reduced with one 31-shuffle transpose-butterfly (lane L ends
-// with score L) instead of G*T separate warp reductions. Online softmax per head, then the partial
-// (o, lse) of every split goes to scratch and a combine kernel merges the splits, writes the fp32
-// output and re-quantises it into q8 blocks for the output projection.
+// with score L) instead of G*T separate warp reductions. Online softmax per head; with several
+// splits each CTA writes its partial (o, lse) to scratch and bumps a per-(row, kv head) counter,
+// and the last CTA to finish merges all splits (independent loads in flight) and writes the
+// output as fp32, bf16 and/or q8 blocks for the output projection — no separate combine launch.
 //
 // KV layout: [num_blocks, n_kv_heads, block_size, head_dim] bf16, so one head's tokens in a block
 // are contiguous (a warp reads whole 256-byte K/V rows).
@@ -152,6 +153,9 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnDecodeArgs a) {
     }
   }
   // ---- merge the 4 warps ----
+  __shared__ float s_fin[G][HD];
+  __shared__ float s_lse[G][64];
+  __shared__ int s_last;
   if (lane == 0) {
 #pragma unroll
     for (int g = 0; g < G; ++g) { s_m[warp][g] = m[g]; s_l[warp][g] = l[g]; }
@@ -162,6 +166,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnDecodeArgs a) {
     for (int i = 0; i < HPL; ++i) s_o[warp][g][lane * HPL + i] = acc[g][i];
   __syncthreads();
   pdl_launch();
+  const bool single = a.num_splits == 1;
   for (int idx = threadIdx.x; idx < G * HD; idx += blockDim.x) {
     const int g = idx / HD, d = idx % HD;
     float M = -INFINITY;
@@ -174,82 +179,95 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnDecodeArgs a) {
       L += s_l[w][g] * f;
       O += s_o[w][g][d] * f;
     }
-    const int h = kvh * G + g;
-    const int64_t base = ((int64_t)r * a.nh + h) * a.num_splits + split;
-    a.part_o[base * HD + d] = L > 0.f ? O / L : 0.f;
-    if (d == 0) a.part_lse[base] = L > 0.f ? M + __logf(L) : -INFINITY;
+    if (single) {
+      if (a.sinks) L += __expf(a.sinks[kvh * G + g] - M);
+      s_fin[g][d] = L > 0.f ? O / L : 0.f;
+    } else {
+      const int h = kvh * G + g;
+      const int64_t base = ((int64_t)r * a.nh + h) * a.num_splits + split;
+      a.part_o[base * HD + d] = L > 0.f ? O / L : 0.f;
+      if (d == 0) a.part_lse[base] = L > 0.f ? M + __logf(L) : -INFINITY;
+    }
   }
-}
-
-// Merge splits: one warp per (row, head). Writes fp32 output and/or q8 blocks.
-template <int HPL>
-__global__ void __launch_bounds__(128) attn_combine_kernel(AttnDecodeArgs a) {
-  constexpr int HD = HPL * 32;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t pair = (int64_t)blockIdx.x * 4 + warp;
-  if (pair >= (int64_t)a.R * a.nh) return;
-  pdl_wait();
-  const int r = (int)(pair / a.nh), h = (int)(pair % a.nh);
-  const int64_t base = pair * a.num_splits;
-  float M = -INFINITY;
-  for (int s = 0; s < a.num_splits; ++s) M = fmaxf(M, a.part_lse[base + s]);
-  if (a.sinks) M = fmaxf(M, a.sinks[h]);
-  float o[HPL] = {};
-  float L = 0.f;
-  for (int s = 0; s < a.num_splits; ++s) {
-    const float lse = a.part_lse[base + s];
-    if (lse == -INFINITY) continue;
-    const float f = __expf(lse - M);
-    L += f;
-    const float* po = a.part_o + (base + s) * HD + lane * HPL;
-#pragma unroll
-    for (int i = 0; i < HPL; ++i) o[i] = fmaf(f, po[i], o[i]);
+  if (!single) {
+    // The last split CTA of this (row, kv head) merges every split (threadfence reduction).
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const int prev = atomicAdd(&a.counters[r * a.nkv + kvh], 1);
+      s_last = prev == a.num_splits - 1;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    const int S = a.num_splits;
+    for (int idx = threadIdx.x; idx < G * S; idx += blockDim.x) {
+      const int g = idx / S, sp = idx % S;
+      s_lse[g][sp] = __ldcg(a.part_lse + ((int64_t)r * a.nh + kvh * G + g) * S + sp);
+    }
+    __syncthreads();
+    if (threadIdx.x < G) {  // per-head max and normaliser; weights stored back in s_lse
+      const int g = threadIdx.x;
+      float M = -INFINITY;
+      for (int sp = 0; sp < S; ++sp) M = fmaxf(M, s_lse[g][sp]);
+      if (a.sinks) M = fmaxf(M, a.sinks[kvh * G + g]);
+      float L = 0.f;
+      for (int sp = 0; sp < S; ++sp) {
+        const float f = s_lse[g][sp] == -INFINITY ? 0.f : __expf(s_lse[g][sp] - M);
+        s_lse[g][sp] = f;
+        L += f;
+      }
+      if (a.sinks) L += __expf(a.sinks[kvh * G + g] - M);
+      s_m[0][g] = L > 0.f ? 1.f / L : 0.f;
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < G * HD; idx += blockDim.x) {
+      const int g = idx / HD, d = idx % HD;
+      const float* po = a.part_o + (((int64_t)r * a.nh + kvh * G + g) * S) * HD + d;
+      float O0 = 0.f, O1 = 0.f, O2 = 0.f, O3 = 0.f;
+      int sp = 0;
+      for (; sp + 4 <= S; sp += 4) {  // independent loads in flight
+        O0 = fmaf(s_lse[g][sp], __ldcg(po + (int64_t)sp * HD), O0);
+        O1 = fmaf(s_lse[g][sp + 1], __ldcg(po + (int64_t)(sp + 1) * HD), O1);
+        O2 = fmaf(s_lse[g][sp + 2], __ldcg(po + (int64_t)(sp + 2) * HD), O2);
+        O3 = fmaf(s_lse[g][sp + 3], __ldcg(po + (int64_t)(sp + 3) * HD), O3);
+      }
+      for (; sp < S; ++sp) O0 = fmaf(s_lse[g][sp], __ldcg(po + (int64_t)sp * HD), O0);
+      s_fin[g][d] = (O0 + O1 + O2 + O3) * s_m[0][g];
+    }
+    if (threadIdx.x == 0) a.counters[r * a.nkv + kvh] = 0;  // ready for the next launch
+    __syncthreads();
+  } else {
+    __syncthreads();
   }
-  if (a.sinks) L += __expf(a.sinks[h] - M);
-  const float inv = L > 0.f ? 1.f / L : 0.f;
-#pragma unroll
-  for (int i = 0; i < HPL; ++i) o[i] *= inv;
-  const int64_t col0 = (int64_t)h * HD + lane * HPL;
+  // ---- final outputs of the G heads: fp32 / bf16 / q8 blocks of 32 dims ----
   const int64_t width = (int64_t)a.nh * HD;
-  if (a.out) {
-#pragma unroll
-    for (int i = 0; i < HPL; ++i) a.out[(int64_t)r * width + col0 + i] = o[i];
-  }
-  if (a.out_bf16) {
-#pragma unroll
-    for (int i = 0; i < HPL; ++i) a.out_bf16[(int64_t)r * width + col0 + i] = __float2bfloat16(o[i]);
+  const int64_t col0 = (int64_t)kvh * G * HD;
+  for (int idx = threadIdx.x; idx < G * HD; idx += blockDim.x) {
+    const float v = s_fin[idx / HD][idx % HD];
+    if (a.out) a.out[(int64_t)r * width + col0 + idx] = v;
+    if (a.out_bf16) a.out_bf16[(int64_t)r * width + col0 + idx] = __float2bfloat16(v);
   }
   if (a.oq) {
-    // A q8 block of 32 dims spans 32/HPL lanes.
-    float amax = 0.f;
-#pragma unroll
-    for (int i = 0; i < HPL; ++i) amax = fmaxf(amax, fabsf(o[i]));
-    constexpr int LPB = 32 / HPL;
-#pragma unroll
-    for (int off = LPB / 2; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-    const float d = amax / 127.f;
-    int qs = 0;
-#pragma unroll
-    for (int i = 0; i < HPL; ++i) {
-      const int qv = amax > 0.f ? __float2int_rn(o[i] / d) : 0;
-      qs += qv;
-      a.oq[(int64_t)r * width + col0 + i] = (int8_t)qv;
-    }
-#pragma unroll
-    for (int off = LPB / 2; off > 0; off >>= 1) qs += __shfl_xor_sync(0xffffffffu, qs, off);
-    if ((lane % LPB) == 0) {
-      const int64_t blk = (col0 >> 5);
-      a.od[(int64_t)r * (width / 32) + blk] = d;
-      a.os[(int64_t)r * (width / 32) + blk] = d * (float)qs;
+    for (int blk = warp; blk < G * HD / 32; blk += 4) {
+      const int idx = blk * 32 + lane;
+      const float v = s_fin[idx / HD][idx % HD];
+      const float amax = warp_max(fabsf(v));
+      const float dq = amax / 127.f;
+      const int qv = amax > 0.f ? __float2int_rn(v / dq) : 0;
+      const float qsum = warp_sum((float)qv);
+      a.oq[(int64_t)r * width + col0 + idx] = (int8_t)qv;
+      if (lane == 0) {
+        a.od[(int64_t)r * (width / 32) + (col0 >> 5) + blk] = dq;
+        a.os[(int64_t)r * (width / 32) + (col0 >> 5) + blk] = dq * qsum;
+      }
     }
   }
-  pdl_launch();
 }
 
 template <int G, int HPL>
 static void launch_g(const AttnDecodeArgs& a, cudaStream_t s, bool pdl) {
   launch(attn_decode_kernel<G, HPL>, dim3(a.num_splits, a.nkv, a.R), dim3(128), 0, s, pdl, a);
-  launch(attn_combine_kernel<HPL>, dim3((a.R * a.nh + 3) / 4), dim3(128), 0, s, pdl, a);
 }
 
 template <int HPL>
@@ -268,6 +286,8 @@ static void launch_hpl(const AttnDecodeArgs& a, int G, cudaStream_t s, bool pdl)
 
 void attention_decode_launch(const AttnDecodeArgs& a, cudaStream_t s, bool pdl) {
   if (a.nh % a.nkv) throw std::runtime_error("attention: n_heads must be a multiple of n_kv_heads");
+  if (a.num_splits > 64) throw std::runtime_error("attention: at most 64 splits");
+  if (a.num_splits > 1 && !a.counters) throw std::runtime_error("attention: split-KV needs the counter scratch");
   const int G = a.nh / a.nkv;
   switch (a.hd) {
     case 64: launch_hpl<2>(a, G, s, pdl); break;

@@ -73,10 +73,11 @@ void rmsnorm_launch(const float* x, int64_t x_stride, const float* w, float eps,
 }
 
 // ---- RoPE + paged KV append -----------------------------------------------------------------
-// One CTA per query row; warp per head (q heads, then k heads, then v heads).
+// Grid (head groups, rows); one warp per head (q heads, then k heads, then v heads), so every
+// head is a single round trip.
 __global__ void __launch_bounds__(256) rope_append_kernel(RopeAppendArgs a) {
   pdl_wait();
-  const int r = blockIdx.x;
+  const int r = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   const int pos = a.positions[r];
   int64_t slot = -1;
@@ -87,7 +88,7 @@ __global__ void __launch_bounds__(256) rope_append_kernel(RopeAppendArgs a) {
   const int hd = a.hd, half = a.rot_dim / 2;
   const float* rope = a.rope + (int64_t)pos * half * 2;
   const int nheads = a.nh + 2 * a.nkv;
-  for (int h = warp; h < nheads; h += nw) {
+  for (int h = blockIdx.x * nw + warp; h < nheads; h += gridDim.x * nw) {
     const int kind = h < a.nh ? 0 : (h < a.nh + a.nkv ? 1 : 2);  // q, k, v
     const float* src = a.qkv + (int64_t)r * a.qkv_stride + (int64_t)h * hd;
     const float* bias = a.bias ? a.bias + (int64_t)h * hd : nullptr;
@@ -143,7 +144,8 @@ __global__ void __launch_bounds__(256) rope_append_kernel(RopeAppendArgs a) {
 
 void rope_append_launch(const RopeAppendArgs& a, cudaStream_t s, bool pdl) {
   if (a.hd % 32 || a.hd > 256) throw std::runtime_error("rope_append: head_dim must be a multiple of 32, <= 256");
-  launch(rope_append_kernel, dim3(a.R), dim3(256), 0, s, pdl, a);
+  const int heads = a.nh + 2 * a.nkv;
+  launch(rope_append_kernel, dim3((heads + 7) / 8, a.R), dim3(256), 0, s, pdl, a);
 }
 
 // ---- SwiGLU over a fused gate|up GEMM output ---------------------------------------------------

@@ -1,19 +1,19 @@
 // Small-batch dequant GEMV (K1, bs 1..8): y[b, n] = sum_k W[n, k] * x[b, k] with W in a GGUF
 // block format dequantised in registers and x as q8 activation blocks, int8 dot products (dp4a).
 //
-// Design: one warp per output row (RPW rows per warp), lanes stride over 128-element units of
-// the row so a warp streams each weight row exactly once with 16-byte loads that bypass L1.
-// Rows are independent, so the grid is N / (8 * RPW) CTAs of 8 warps — many resident CTAs per
-// SM keep enough bytes in flight to saturate HBM. The activation columns (a few KB) are read
-// through the read-only path and stay in L1/L2. Programmatic dependent launch: the first weight
-// unit of every row is fetched before waiting on the producer kernel.
-//
-// Epilogues: STORE (y), RESID (x += y, fp32 residual stream), SWIGLU_Q8 (pair mode: gate and up
-// rows, h = silu(g) * u, re-quantised to q8 blocks for the down projection).
+// Decode at batch 1 is a chain of dependent kernels, so each kernel's critical path is kept to
+// one round trip to memory:
+//  * one warp per output row (a gate/up row pair for SwiGLU); every lane issues all of its weight
+//    loads (16-byte, L1-bypassing) before anything else, and the first loads are issued before
+//    the programmatic-dependent-launch wait, overlapping the previous kernel's tail;
+//  * the input can be the fp32 residual stream: the CTA then computes RMSNorm and the q8 blocks
+//    itself into shared memory (XIN_NORM), removing the separate normalisation kernel;
+//  * the SwiGLU variant runs 32 warps per CTA so its 32 rows form one q8 block of the output.
+// Epilogues: STORE (y), RESID (y += acc, fp32 residual stream), SWIGLU_Q8 (h = silu(g) * u -> q8).
 //
 // Parity: replaces the reference's Q4_K/Q6_K/Q8_0 GEMV family (crates/hawking-core/shaders/quant.metal,
-// gemm_q4_k_m_fused*, _pair* gate+up with SwiGLU, _add residual-fused variants); numerics oracle
-// crates/hawking-core/src/quant.rs:722 (gemv_q4_k_q8k).
+// gemm_q4_k_m_fused*, _pair* gate+up with SwiGLU, _add residual-fused variants, add_rmsnorm_fused_q8
+// feeding them); numerics oracle crates/hawking-core/src/quant.rs:722 (gemv_q4_k_q8k).
 #include "gemv.cuh"
 
 namespace hk {
@@ -43,67 +43,156 @@ __device__ __forceinline__ float dot_unit(const typename UnitOf<FMT>::T& r, int 
   else return dot_unit_q6k(r, u, xq, xd, xs);
 }
 
-// Sum over the row for NB activation columns; the result is complete on every lane.
-template <int FMT, int NB>
-__device__ __forceinline__ void row_dot(const WPlanes& w, int64_t row, int n_units, const XQ& x, float (&acc)[NB],
-                                        bool prefetched, const typename UnitOf<FMT>::T& first) {
+// Units (128 elements) per lane: 1 covers K <= 4096 with one batch of loads, 4 covers K <= 16384.
+constexpr int kMaxUnitsPerLane = 4;
+
+// The activation source of one launch, resolved to plain pointers (global or shared memory).
+struct XSrc {
+  const int8_t* q;
+  const float* d;
+  const float* s;
+  int64_t sq, ss;  // per-column strides
+};
+
+// Row dot over NB columns with all of the lane's weight units loaded up front (u = lane + 32 j).
+template <int FMT, int NB, int UPL>
+__device__ __forceinline__ void row_dot_batched(typename UnitOf<FMT>::T (&r)[UPL], int n_units,
+                                                const XSrc& x, int nb, float (&acc)[NB]) {
   const int lane = threadIdx.x & 31;
 #pragma unroll
   for (int b = 0; b < NB; ++b) acc[b] = 0.f;
-  int u = lane;
-  if (prefetched && u < n_units) {
 #pragma unroll
-    for (int b = 0; b < NB; ++b)
-      acc[b] += dot_unit<FMT>(first, u, x.q + b * x.stride_q, x.d + b * x.stride_s, x.s + b * x.stride_s);
-    u += 32;
+  for (int j = 0; j < UPL; ++j) {
+    const int u = lane + 32 * j;
+    if (u < n_units) {
+#pragma unroll
+      for (int b = 0; b < NB; ++b) {
+        const int bb = b < nb ? b : 0;  // padded columns recompute column 0 and are discarded
+        acc[b] += dot_unit<FMT>(r[j], u, x.q + bb * x.sq, x.d + bb * x.ss, x.s + bb * x.ss);
+      }
+    }
   }
-#pragma unroll 2
-  for (; u < n_units; u += 32) {
-    typename UnitOf<FMT>::T r;
-    load_unit<FMT>(w, row, u, r);
-#pragma unroll
-    for (int b = 0; b < NB; ++b)
-      acc[b] += dot_unit<FMT>(r, u, x.q + b * x.stride_q, x.d + b * x.stride_s, x.s + b * x.stride_s);
-  }
-#pragma unroll
-  for (int b = 0; b < NB; ++b) acc[b] = warp_sum(acc[b]);
 }
 
-template <int FMT, int NB, int EPI>
-__global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
-  constexpr int RPW = (EPI == EPI_SWIGLU_Q8) ? 4 : 1;  // swiglu needs 32 rows per CTA for q8 blocks
+template <int FMT, int UPL>
+__device__ __forceinline__ void load_row(const WPlanes& w, int64_t row, int n_units,
+                                         typename UnitOf<FMT>::T (&r)[UPL]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int j = 0; j < UPL; ++j) {
+    const int u = lane + 32 * j;
+    if (u < n_units) load_unit<FMT>(w, row, u, r[j]);
+  }
+}
+
+// CTA-cooperative RMSNorm + q8 of nb fp32 rows into shared memory. Thread t handles elements
+// t + e * blockDim.x (EPT of them, all loaded before any reduction), so each warp owns whole
+// 32-element blocks. Columns are processed one after another.
+template <int EPT>
+__device__ __forceinline__ void norm_q8_to_smem(const GemvArgs& a, int nb, int8_t* sq, float* sd, float* ss,
+                                                float* red) {
+  const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31;
+  const int K = a.K;
+  float w[EPT];
+#pragma unroll
+  for (int e = 0; e < EPT; ++e) {
+    const int i = tid + e * nt;
+    w[e] = (i < K && a.norm_w) ? a.norm_w[i] : 1.f;
+  }
+  for (int b = 0; b < nb; ++b) {
+    float v[EPT];
+#pragma unroll
+    for (int e = 0; e < EPT; ++e) {
+      const int i = tid + e * nt;
+      v[e] = i < K ? a.x_f32[(int64_t)b * a.x_f32_stride + i] : 0.f;
+    }
+    float scale = 1.f;
+    if (a.norm) {
+      float s2 = 0.f;
+#pragma unroll
+      for (int e = 0; e < EPT; ++e) s2 += v[e] * v[e];
+      s2 = warp_sum(s2);
+      if (lane == 0) red[b * 32 + (tid >> 5)] = s2;
+      __syncthreads();
+      s2 = lane < (nt >> 5) ? red[b * 32 + lane] : 0.f;
+      s2 = warp_sum(s2);
+      scale = rsqrtf(s2 / K + a.eps);
+    }
+#pragma unroll
+    for (int e = 0; e < EPT; ++e) {
+      const int i = tid + e * nt;
+      if (i < K) {  // K % 32 == 0 and nt % 32 == 0: whole warps are in or out
+        const float x = v[e] * scale * w[e];
+        const float amax = warp_max(fabsf(x));
+        const float d = amax / 127.f;
+        const int q = amax > 0.f ? __float2int_rn(x / d) : 0;
+        const float qs = warp_sum((float)q);
+        sq[b * K + i] = (int8_t)q;
+        if (lane == 0) {
+          sd[b * (K / 32) + (i >> 5)] = d;
+          ss[b * (K / 32) + (i >> 5)] = d * qs;
+        }
+      }
+    }
+  }
+  __syncthreads();
+}
+
+// Kernel: one warp per row (STORE / RESID) or per gate/up row pair (SWIGLU_Q8, 32 warps).
+template <int FMT, int NB, int EPI, int XIN, int UPL>
+__global__ void __launch_bounds__(EPI == EPI_SWIGLU_Q8 ? 1024 : 256) gemv_kernel(GemvArgs a, int nb) {
+  extern __shared__ __align__(16) uint8_t gsm[];
+  __shared__ float red[8 * 32];
+  __shared__ float hbuf[NB][32];
+  constexpr int WARPS = EPI == EPI_SWIGLU_Q8 ? 32 : 8;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_units = a.K / 128;
-  const int64_t row0 = ((int64_t)blockIdx.x * 8 + warp) * RPW;
+  const int64_t row = (int64_t)blockIdx.x * WARPS + warp;
+  const bool live = row < a.N;
 
-  // Prefetch the first unit of the first row before the producer finishes.
-  typename UnitOf<FMT>::T first;
-  const bool pf = row0 < a.N && lane < n_units;
-  if (pf) load_unit<FMT>(a.w0, row0, lane, first);
+  // 1) weights first (do not depend on the producer kernel)
+  typename UnitOf<FMT>::T wg[UPL];
+  typename UnitOf<FMT>::T wu[EPI == EPI_SWIGLU_Q8 ? UPL : 1];
+  if (live) {
+    load_row<FMT, UPL>(a.w0, row, n_units, wg);
+    if constexpr (EPI == EPI_SWIGLU_Q8) load_row<FMT, UPL>(a.w1, row, n_units, wu);
+  }
   pdl_wait();
 
-  XQ x{a.xq, a.xd, a.xs, a.x_stride_q, a.x_stride_s};
+  // 2) activations
+  XSrc x;
+  if constexpr (XIN == XIN_NORM) {
+    int8_t* sq = reinterpret_cast<int8_t*>(gsm);
+    float* sd = reinterpret_cast<float*>(gsm + nb * a.K);
+    float* ss = sd + nb * (a.K / 32);
+    constexpr int NT = WARPS * 32;
+    constexpr int EPT = (4096 + NT - 1) / NT;  // elements per thread, K <= 4096 on this path
+    norm_q8_to_smem<EPT>(a, nb, sq, sd, ss, red);
+    x = XSrc{sq, sd, ss, a.K, a.K / 32};
+  } else {
+    x = XSrc{a.xq, a.xd, a.xs, a.x_stride_q, a.x_stride_s};
+  }
+
+  // 3) dot products + epilogue
   if constexpr (EPI == EPI_SWIGLU_Q8) {
-    __shared__ float hbuf[NB][32];
-    typename UnitOf<FMT>::T dummy;
+    float g[NB], u[NB];
+    if (live) {
+      row_dot_batched<FMT, NB, UPL>(wg, n_units, x, nb, g);
+      row_dot_batched<FMT, NB, UPL>(wu, n_units, x, nb, u);
+    }
 #pragma unroll
-    for (int r = 0; r < RPW; ++r) {
-      const int64_t row = row0 + r;
-      float g[NB], u[NB];
-      if (row < a.N) {
-        row_dot<FMT, NB>(a.w0, row, n_units, x, g, r == 0 && pf, first);
-        row_dot<FMT, NB>(a.w1, row, n_units, x, u, false, dummy);
-      }
-      if (lane == 0) {
+    for (int b = 0; b < NB; ++b) {
+      g[b] = live ? warp_sum(g[b]) : 0.f;
+      u[b] = live ? warp_sum(u[b]) : 0.f;
+    }
+    if (lane == 0) {
 #pragma unroll
-        for (int b = 0; b < NB; ++b)
-          hbuf[b][warp * RPW + r] = row < a.N ? g[b] / (1.f + __expf(-g[b])) * u[b] : 0.f;
-      }
+      for (int b = 0; b < NB; ++b) hbuf[b][warp] = live ? g[b] / (1.f + __expf(-g[b])) * u[b] : 0.f;
     }
     __syncthreads();
     pdl_launch();
-    // Warp b quantises column b's 32 values (one q8 block).
-    for (int b = warp; b < NB; b += 8) {
+    if (warp < nb) {
+      const int b = warp;
       const int64_t n = (int64_t)blockIdx.x * 32 + lane;
       const float v = hbuf[b][lane];
       const float amax = warp_max(fabsf(v));
@@ -117,59 +206,79 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs a) {
       }
     }
   } else {
-    if (row0 >= a.N) { pdl_launch(); return; }
+    if (!live) { pdl_launch(); return; }
     float acc[NB];
-    row_dot<FMT, NB>(a.w0, row0, n_units, x, acc, pf, first);
+    row_dot_batched<FMT, NB, UPL>(wg, n_units, x, nb, acc);
+#pragma unroll
+    for (int b = 0; b < NB; ++b) acc[b] = warp_sum(acc[b]);
     pdl_launch();
-    if (lane < NB) {
+    if (lane < nb) {
       float v = acc[0];
 #pragma unroll
       for (int b = 1; b < NB; ++b)
         if (lane == b) v = acc[b];
-      float* y = a.y + (int64_t)lane * a.y_stride + row0;
-      if (a.bias) v += a.bias[row0];
+      float* y = a.y + (int64_t)lane * a.y_stride + row;
+      if (a.bias) v += a.bias[row];
       if constexpr (EPI == EPI_RESID) *y += v;
       else *y = v;
     }
   }
 }
 
-template <int FMT, int EPI>
+template <int FMT, int EPI, int XIN, int UPL>
 static void dispatch_nb(const GemvArgs& a, int nb, cudaStream_t s, bool pdl) {
   const int rows_per_cta = (EPI == EPI_SWIGLU_Q8) ? 32 : 8;
-  dim3 grid((a.N + rows_per_cta - 1) / rows_per_cta), block(256);
-#define HK_NB(n) \
-  case n: launch(gemv_kernel<FMT, n, EPI>, grid, block, 0, s, pdl, a); break;
-  switch (nb) {
-    HK_NB(1) HK_NB(2) HK_NB(3) HK_NB(4) HK_NB(5) HK_NB(6) HK_NB(7) HK_NB(8)
-    default: throw std::runtime_error("gemv: batch columns must be 1..8");
-  }
-#undef HK_NB
+  const int threads = (EPI == EPI_SWIGLU_Q8) ? 1024 : 256;
+  dim3 grid((a.N + rows_per_cta - 1) / rows_per_cta), block(threads);
+  const size_t smem = XIN == XIN_NORM ? (size_t)nb * a.K + 2 * (size_t)nb * (a.K / 32) * 4 : 0;
+  auto go = [&](auto kern) {
+    if (smem > 48 * 1024) HK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    launch(kern, grid, block, smem, s, pdl, a, nb);
+  };
+  if (nb == 1) go(gemv_kernel<FMT, 1, EPI, XIN, UPL>);
+  else if (nb == 2) go(gemv_kernel<FMT, 2, EPI, XIN, UPL>);
+  else if (nb <= 4) go(gemv_kernel<FMT, 4, EPI, XIN, UPL>);
+  else if (nb <= 8) go(gemv_kernel<FMT, 8, EPI, XIN, UPL>);
+  else throw std::runtime_error("gemv: batch columns must be 1..8");
 }
 
-template <int EPI>
+template <int EPI, int XIN, int UPL>
 static void dispatch_fmt(int fmt, const GemvArgs& a, int nb, cudaStream_t s, bool pdl) {
   switch (fmt) {
-    case WF_Q4_K: dispatch_nb<WF_Q4_K, EPI>(a, nb, s, pdl); break;
-    case WF_Q4_0: dispatch_nb<WF_Q4_0, EPI>(a, nb, s, pdl); break;
-    case WF_Q8_0: dispatch_nb<WF_Q8_0, EPI>(a, nb, s, pdl); break;
-    case WF_Q5_0: dispatch_nb<WF_Q5_0, EPI>(a, nb, s, pdl); break;
-    case WF_Q6_K: dispatch_nb<WF_Q6_K, EPI>(a, nb, s, pdl); break;
+    case WF_Q4_K: dispatch_nb<WF_Q4_K, EPI, XIN, UPL>(a, nb, s, pdl); break;
+    case WF_Q4_0: dispatch_nb<WF_Q4_0, EPI, XIN, UPL>(a, nb, s, pdl); break;
+    case WF_Q8_0: dispatch_nb<WF_Q8_0, EPI, XIN, UPL>(a, nb, s, pdl); break;
+    case WF_Q5_0: dispatch_nb<WF_Q5_0, EPI, XIN, UPL>(a, nb, s, pdl); break;
+    case WF_Q6_K: dispatch_nb<WF_Q6_K, EPI, XIN, UPL>(a, nb, s, pdl); break;
     default: throw std::runtime_error("gemv: unsupported weight format " + std::to_string(fmt));
   }
 }
 
 void gemv_launch(int fmt, int epi, const GemvArgs& a, int nb, cudaStream_t s, bool pdl) {
   if (a.K % 128) throw std::runtime_error("gemv: K must be a multiple of 128");
-  if (fmt == WF_Q4_K || fmt == WF_Q6_K) {
-    if (a.K % 256) throw std::runtime_error("gemv: K-quant rows must be a multiple of 256");
+  if ((fmt == WF_Q4_K || fmt == WF_Q6_K) && a.K % 256) throw std::runtime_error("gemv: K-quant rows need K % 256 == 0");
+  if (a.K > kMaxUnitsPerLane * 32 * 128) throw std::runtime_error("gemv: K too large");
+  const bool small_k = a.K <= 32 * 128;
+  if (epi == EPI_SWIGLU_Q8 && a.N % 32) throw std::runtime_error("gemv swiglu: N must be a multiple of 32");
+  if (a.x_f32) {  // fused RMSNorm -> q8 prologue (K <= 4096)
+    if (!small_k) throw std::runtime_error("gemv: the fused-norm input path needs K <= 4096");
+    if (epi == EPI_STORE) dispatch_fmt<EPI_STORE, XIN_NORM, 1>(fmt, a, nb, s, pdl);
+    else if (epi == EPI_SWIGLU_Q8) dispatch_fmt<EPI_SWIGLU_Q8, XIN_NORM, 1>(fmt, a, nb, s, pdl);
+    else throw std::runtime_error("gemv: fused-norm input supports STORE and SWIGLU_Q8");
+    return;
   }
   switch (epi) {
-    case EPI_STORE: dispatch_fmt<EPI_STORE>(fmt, a, nb, s, pdl); break;
-    case EPI_RESID: dispatch_fmt<EPI_RESID>(fmt, a, nb, s, pdl); break;
+    case EPI_STORE:
+      if (small_k) dispatch_fmt<EPI_STORE, XIN_Q8, 1>(fmt, a, nb, s, pdl);
+      else dispatch_fmt<EPI_STORE, XIN_Q8, 4>(fmt, a, nb, s, pdl);
+      break;
+    case EPI_RESID:
+      if (small_k) dispatch_fmt<EPI_RESID, XIN_Q8, 1>(fmt, a, nb, s, pdl);
+      else dispatch_fmt<EPI_RESID, XIN_Q8, 4>(fmt, a, nb, s, pdl);
+      break;
     case EPI_SWIGLU_Q8:
-      if (a.N % 32) throw std::runtime_error("gemv swiglu: N must be a multiple of 32");
-      dispatch_fmt<EPI_SWIGLU_Q8>(fmt, a, nb, s, pdl);
+      if (!small_k) throw std::runtime_error("gemv swiglu: K <= 4096");
+      dispatch_fmt<EPI_SWIGLU_Q8, XIN_Q8, 1>(fmt, a, nb, s, pdl);
       break;
     default: throw std::runtime_error("gemv: bad epilogue");
   }

@@ -209,6 +209,7 @@ class LlamaModel:
         cap = max(r * self.num_splits(r) for r in range(1, R + 1))
         self.part_o = torch.zeros(cap * nh * hd, device=self.dev)
         self.part_lse = torch.zeros(cap * nh, device=self.dev)
+        self.attn_counters = torch.zeros(R * nkv, dtype=torch.int32, device=self.dev)
         self.logits = torch.zeros(R, cfg.vocab, device=self.dev)
         # tensor-core path buffers (bf16 activations; fp32 outputs kept zeroed between uses)
         self.xb = torch.zeros(R, H, dtype=torch.bfloat16, device=self.dev)
@@ -263,12 +264,12 @@ class LlamaModel:
                 self._ffn_block_tc(lw, rows)
             else:
                 self._attention_block_gemv(l, lw, rows, splits)
-                ops.rmsnorm_q8(x, lw.ffn_norm, cfg.eps, self.xa.view(rows))
                 if lw.moe is not None:
+                    ops.rmsnorm_q8(x, lw.ffn_norm, cfg.eps, self.xa.view(rows))
                     lw.moe.forward(self, rows)
                 else:
-                    self._gemv_cols(lambda c0, c1: ops.gemv_swiglu(lw.w_gate, lw.w_up, self.xa_view(c0, c1),
-                                                                   self._q8_slice(self.hq, c0, c1)), rows)
+                    self._gemv_cols(lambda c0, c1: ops.gemv_norm_swiglu(
+                        lw.w_gate, lw.w_up, x[c0:c1], lw.ffn_norm, cfg.eps, self._q8_slice(self.hq, c0, c1)), rows)
                     self._gemv_cols(lambda c0, c1: ops.gemv(lw.w_down,
                                                             self._q8_slice(self.hq, c0, c1, lw.w_down.K),
                                                             x[c0:c1], residual=True), rows)
@@ -285,15 +286,11 @@ class LlamaModel:
             self.logits[:nl].zero_()
             ops.tc_gemm(w.lm_head, src, self.logits[:nl], self.status, y_zeroed=True)
         else:
-            ops.rmsnorm_q8(x, w.out_norm, cfg.eps, self.xa.view(rows))
-            xa = self.xa
+            src = x
             if n_logits:
-                idx = self.logit_rows[:nl].long()
-                xa = Q8Act.__new__(Q8Act)
-                xa.K, xa.q, xa.d, xa.s = self.xa.K, self.xa.q.index_select(0, idx), \
-                    self.xa.d.index_select(0, idx), self.xa.s.index_select(0, idx)
-            self._gemv_cols(lambda c0, c1: ops.gemv(w.lm_head, self._q8_slice(xa, c0, c1, cfg.hidden),
-                                                    self.logits[c0:c1]), nl)
+                src = x.index_select(0, self.logit_rows[:nl].long())
+            self._gemv_cols(lambda c0, c1: ops.gemv_norm(w.lm_head, src[c0:c1], w.out_norm, cfg.eps,
+                                                         self.logits[c0:c1]), nl)
         if sample == "greedy":
             ops.argmax(self.logits[:nl], self.next_ids[:nl])
         elif sample == "sample":
@@ -310,17 +307,15 @@ class LlamaModel:
                         eps=cfg.eps, block_tables=kv.block_tables, row_seq=inp.row_seq[:rows])
         ops.attention_decode(self.q[:rows], kv.k[l], kv.v[l], kv.block_tables, inp.row_seq[:rows],
                              inp.row_ctx[:rows], self.scale, splits, self.part_o, self.part_lse,
-                             out_q8=out_q8, out_bf16=out_bf16)
+                             out_q8=out_q8, out_bf16=out_bf16, counters=self.attn_counters)
 
     def _attention_block_gemv(self, l, lw, rows, splits):
         x = self.x[:rows]
-        ops.rmsnorm_q8(x, lw.attn_norm, self.cfg.eps, self.xa.view(rows))
 
         def qkv_fn(c0, c1):
-            xa = self.xa_view(c0, c1)
             off = 0
             for wt in lw.wqkv:
-                ops.gemv(wt, xa, self.qkv[c0:c1, off:off + wt.N])
+                ops.gemv_norm(wt, x[c0:c1], lw.attn_norm, self.cfg.eps, self.qkv[c0:c1, off:off + wt.N])
                 off += wt.N
         self._gemv_cols(qkv_fn, rows)
         self._rope_attention(l, lw, rows, splits, out_q8=self.att.view(rows))

@@ -63,13 +63,27 @@ def rmsnorm(x, w, eps, yf=None, yb=None):
 def gemv(w: QWeight, x: Q8Act, y: torch.Tensor, residual: bool = False, bias=None):
     launches.add()
     kernels().gemv(w.fmt, EPI_RESID if residual else EPI_STORE, w.planes, [], w.N, w.K, x.q, x.d, x.s, y, bias,
-                   None, None, None, PDL)
+                   None, None, None, None, None, -1.0, PDL)
 
 
 def gemv_swiglu(w_gate: QWeight, w_up: QWeight, x: Q8Act, out: Q8Act):
     launches.add()
     kernels().gemv(w_gate.fmt, EPI_SWIGLU_Q8, w_gate.planes, w_up.planes, w_gate.N, w_gate.K, x.q, x.d, x.s, None,
-                   None, out.q, out.d, out.s, PDL)
+                   None, out.q, out.d, out.s, None, None, -1.0, PDL)
+
+
+def gemv_norm(w: QWeight, x: torch.Tensor, norm_w, eps: float, y: torch.Tensor, bias=None):
+    """y = W @ q8(rmsnorm(x) * norm_w): the norm and activation quantisation run inside the GEMV
+    (each CTA normalises the fp32 rows itself while its weight loads are in flight)."""
+    launches.add()
+    kernels().gemv(w.fmt, EPI_STORE, w.planes, [], w.N, w.K, None, None, None, y, bias, None, None, None, x, norm_w,
+                   eps, PDL)
+
+
+def gemv_norm_swiglu(w_gate: QWeight, w_up: QWeight, x: torch.Tensor, norm_w, eps: float, out: Q8Act):
+    launches.add()
+    kernels().gemv(w_gate.fmt, EPI_SWIGLU_Q8, w_gate.planes, w_up.planes, w_gate.N, w_gate.K, None, None, None,
+                   None, None, out.q, out.d, out.s, x, norm_w, eps, PDL)
 
 
 def rope_table(max_pos: int, rot_dim: int, theta: float, freq_factors: Optional[torch.Tensor] = None,
@@ -99,11 +113,14 @@ def advance(ids, next_ids, positions, row_ctx, rows: int):
 
 
 def attention_decode(q, k_cache, v_cache, block_tables, row_seq, row_ctx, scale, num_splits, part_o, part_lse,
-                     out=None, out_q8: Optional[Q8Act] = None, sinks=None, out_bf16=None):
-    launches.add(2)
+                     out=None, out_q8: Optional[Q8Act] = None, sinks=None, out_bf16=None, counters=None):
+    """Split-KV paged decode attention. With num_splits > 1 the scratch (part_o, part_lse and the
+    zero-initialised int32 ``counters`` [rows * n_kv_heads]) carries the per-split partials; the
+    last split CTA of each (row, kv head) merges them."""
+    launches.add(1)
     kernels().attention_decode(q, k_cache, v_cache, block_tables, row_seq, row_ctx, scale, num_splits, part_o,
                                part_lse, out, out_q8.q if out_q8 else None, out_q8.d if out_q8 else None,
-                               out_q8.s if out_q8 else None, sinks, out_bf16, PDL)
+                               out_q8.s if out_q8 else None, sinks, out_bf16, counters, PDL)
 
 
 def argmax(logits: torch.Tensor, out: torch.Tensor):

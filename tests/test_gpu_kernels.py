@@ -149,7 +149,10 @@ def test_attention_decode(nh, nkv, hd, splits):
     part_l = torch.zeros(R * nh * splits, device=DEV)
     out = torch.zeros(R, nh * hd, device=DEV)
     oq = Q8Act(R, nh * hd, DEV)
-    ops.attention_decode(q, kc, vc, tables, row_seq, row_ctx, scale, splits, part_o, part_l, out=out, out_q8=oq)
+    counters = torch.zeros(R * nkv, dtype=torch.int32, device=DEV)
+    ops.attention_decode(q, kc, vc, tables, row_seq, row_ctx, scale, splits, part_o, part_l, out=out, out_q8=oq,
+                         counters=counters)
+    assert counters.abs().sum().item() == 0  # reset by the merging CTAs
     ref = _paged_attention_ref(q, kc, vc, tables, row_seq, row_ctx, scale).reshape(R, -1)
     torch.testing.assert_close(out, ref, rtol=2e-3, atol=2e-3)
     assert ((oq.dequantize() - ref).abs() <= oq.d.repeat_interleave(32, 1) * 0.51 + 3e-3).all()
