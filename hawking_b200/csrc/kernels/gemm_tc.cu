@@ -20,6 +20,8 @@
 // Q4_K GEMM used by forward_tokens_batch_tcb / multiseq decode, crates/hawking-core/src/model/qwen_dense.rs:7569).
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
+
 #include "api.h"
 #include "qformats.cuh"
 #include "sm100.cuh"
@@ -60,6 +62,7 @@ struct TcArgs {
   float* y;
   int64_t y_stride;
   int atomic;
+  int serialize;
   int* status;
 };
 
@@ -169,6 +172,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             umma_f16(tmem, ad, bd, idesc, (i | c | kk) != 0);
           }
         umma_commit(&a_empty[slot]);
+        if (a.serialize) ok = mbar_wait(&a_empty[slot], (i / DA) & 1, a.status);  // debug: no MMA/dequant overlap
       }
       umma_commit(acc_full);
     } else if (warp >= kDequantWarp0 && warp < kDequantWarp0 + kDequantWarps) {
@@ -182,8 +186,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint4 hdr = *reinterpret_cast<const uint4*>(smem + L::off_hdr + rs * RAW_HDR + r * 16);
         const uint4 q0 = *reinterpret_cast<const uint4*>(smem + L::off_qs + rs * RAW_QS + r * 64 + c * 32);
         const uint4 q1 = *reinterpret_cast<const uint4*>(smem + L::off_qs + rs * RAW_QS + r * 64 + c * 32 + 16);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&raw_empty[rs]);
         const int gs = s0 + i, h = gs & 1;
         const int j0 = 4 * h + 2 * c;
         int sc0, mn0, sc1, mn1;
@@ -207,7 +209,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&a_full[as]);
+        if (lane == 0) {
+          mbar_arrive(&a_full[as]);
+          mbar_arrive(&raw_empty[rs]);  // raw values were consumed above
+        }
       }
     }
 
@@ -295,6 +300,7 @@ void launch_bn(const TcGemmArgs& g, cudaStream_t s) {
   a.y_stride = g.y_stride;
   a.atomic = (g.atomic || splits > 1) ? 1 : 0;
   a.status = g.status;
+  a.serialize = getenv("HK_GEMM_SERIALIZE") != nullptr;
   static bool attr_set = false;
   if (!attr_set) {
     HK_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_q4k_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::total));

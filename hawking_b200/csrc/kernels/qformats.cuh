@@ -20,7 +20,9 @@
 namespace hk {
 
 
-__device__ __forceinline__ int4 ldx16(const int8_t* p) { return __ldg(reinterpret_cast<const int4*>(p)); }
+// Activation loads use generic addressing: the q8 input may live in global or shared memory.
+__device__ __forceinline__ int4 ldx16(const int8_t* p) { return *reinterpret_cast<const int4*>(p); }
+__device__ __forceinline__ float ldxf(const float* p) { return *p; }
 
 // Q4_K/Q5_K six-bit scale & min of sub-block j (0..7) from the 12 scale bytes packed in 3 words.
 __device__ __forceinline__ void q4k_scale_min(int j, uint32_t s0, uint32_t s1, uint32_t s2, int& sc, int& mn) {
@@ -74,7 +76,7 @@ __device__ __forceinline__ float dot_unit_q4k(const UnitQ4K& r, int u, const int
     dot = dp4a((qb.z >> shift) & 0x0F0F0F0F, x1.z, dot);
     dot = dp4a((qb.w >> shift) & 0x0F0F0F0F, x1.w, dot);
     const int blk = (k0 >> 5) + t;
-    acc += d * (float)sc * __ldg(xd + blk) * (float)dot - dmin * (float)mn * __ldg(xs + blk);
+    acc += d * (float)sc * ldxf(xd + blk) * (float)dot - dmin * (float)mn * ldxf(xs + blk);
   }
   return acc;
 }
@@ -110,7 +112,7 @@ __device__ __forceinline__ float dot_unit_q4_0(const UnitQ4_0& r, int u, const i
     const uint32_t dw = b < 2 ? r.d.x : r.d.y;
     const float dwf = __half2float(__ushort_as_half((uint16_t)(dw >> (16 * (b & 1)))));
     const int blk = (k0 >> 5) + b;
-    acc += dwf * (__ldg(xd + blk) * (float)dot - 8.f * __ldg(xs + blk));
+    acc += dwf * (ldxf(xd + blk) * (float)dot - 8.f * ldxf(xs + blk));
   }
   return acc;
 }
@@ -145,7 +147,7 @@ __device__ __forceinline__ float dot_unit_q8_0(const UnitQ8_0& r, int u, const i
     dot = dp4a(qb.w, x1.w, dot);
     const uint32_t dw = b < 2 ? r.d.x : r.d.y;
     const float dwf = __half2float(__ushort_as_half((uint16_t)(dw >> (16 * (b & 1)))));
-    acc += dwf * __ldg(xd + (k0 >> 5) + b) * (float)dot;
+    acc += dwf * ldxf(xd + (k0 >> 5) + b) * (float)dot;
   }
   (void)xs;
   return acc;
@@ -190,7 +192,7 @@ __device__ __forceinline__ float dot_unit_q5_0(const UnitQ5_0& r, int u, const i
     const uint32_t dw = b < 2 ? r.d.x : r.d.y;
     const float dwf = __half2float(__ushort_as_half((uint16_t)(dw >> (16 * (b & 1)))));
     const int blk = (k0 >> 5) + b;
-    acc += dwf * (__ldg(xd + blk) * (float)dot - 16.f * __ldg(xs + blk));
+    acc += dwf * (ldxf(xd + blk) * (float)dot - 16.f * ldxf(xs + blk));
   }
   return acc;
 }
@@ -239,7 +241,7 @@ __device__ __forceinline__ float dot_unit_q6k(const UnitQ6K& r, int u, const int
       xs16[i >> 2] = dp4a(xw[i], 0x01010101, xs16[i >> 2]);
     }
     // Two 16-element sub-blocks per group: scale index 2g + h.
-    const float dx = __ldg(xd + (k0 >> 5) + g);
+    const float dx = ldxf(xd + (k0 >> 5) + g);
     acc += r.d * dx * ((float)sc[2 * g] * (float)(dot16[0] - 32 * xs16[0]) +
                        (float)sc[2 * g + 1] * (float)(dot16[1] - 32 * xs16[1]));
   }

@@ -156,3 +156,34 @@ def tc_gemm(w: QWeight, x: torch.Tensor, y: torch.Tensor, status: torch.Tensor, 
 def swiglu_bf16(gu: torch.Tensor, F: int, h: torch.Tensor, clear: bool = True):
     launches.add()
     kernels().swiglu_bf16(gu, F, h, clear, PDL)
+
+
+# ---- mixture of experts ----
+def router_logits(w: torch.Tensor, x: Q8Act, logits: torch.Tensor):
+    launches.add()
+    kernels().router_logits(w, x.q, x.d, logits, PDL)
+
+
+def moe_topk(logits, bias, k: int, scoring: int, n_groups: int, topk_groups: int, renorm: bool, scale: float,
+             ids, weights):
+    launches.add()
+    kernels().moe_topk(logits, bias, k, scoring, n_groups, topk_groups, renorm, scale, ids, weights, PDL)
+
+
+def moe_align(ids, E: int, x: Q8Act, counts, offsets, sorted_pairs, gathered: Q8Act):
+    launches.add()
+    kernels().moe_align(ids, E, x.q, x.d, x.s, counts, offsets, sorted_pairs, gathered.q, gathered.d, gathered.s, PDL)
+
+
+def moe_gemv_swiglu(w_gate: QWeight, w_up: QWeight, N: int, E: int, k: int, counts, offsets, sorted_pairs,
+                    x: Q8Act, out: Q8Act):
+    launches.add()
+    kernels().moe_gemv(w_gate.fmt, 0, w_gate.planes, w_up.planes, N, w_gate.K, E, k, counts, offsets, sorted_pairs,
+                       x.q, x.d, x.s, out.q, out.d, out.s, None, None, PDL)
+
+
+def moe_gemv_down(w_down: QWeight, N: int, E: int, k: int, counts, offsets, sorted_pairs, h: Q8Act,
+                  y: torch.Tensor, route_w: torch.Tensor):
+    launches.add()
+    kernels().moe_gemv(w_down.fmt, 1, w_down.planes, [], N, w_down.K, E, k, counts, offsets, sorted_pairs,
+                       h.q, h.d, h.s, None, None, None, y, route_w, PDL)
