@@ -198,3 +198,27 @@ def test_embed(fmt):
     out = torch.zeros(3, H, device=DEV)
     ops.embed(w, ids, out)
     torch.testing.assert_close(out, w.dequantize()[ids.long()], rtol=0, atol=1e-6)
+
+
+@pytest.mark.parametrize("K", [512, 1408, 4096])
+@pytest.mark.parametrize("nb", [1, 3])
+def test_gemv_fused_norm_matches_separate(K, nb):
+    fmt = GgmlType.Q4_0 if K % 256 else GgmlType.Q4_K
+    g = torch.Generator(device=DEV).manual_seed(K + nb)
+    N = 256
+    w = QWeight.quantize(torch.randn(N, K, device=DEV, generator=g) * 0.02, fmt)
+    x = torch.randn(nb, K, device=DEV, generator=g) * 3
+    nw = torch.rand(K, device=DEV, generator=g) + 0.5
+    a = Q8Act(nb, K, DEV)
+    ops.rmsnorm_q8(x, nw, 1e-5, a)
+    y_ref = torch.zeros(nb, N, device=DEV)
+    ops.gemv(w, a, y_ref)
+    y = torch.zeros(nb, N, device=DEV)
+    ops.gemv_norm(w, x, nw, 1e-5, y)
+    torch.testing.assert_close(y, y_ref, rtol=1e-4, atol=1e-4 * y_ref.abs().max().item())
+    # SwiGLU pair through the fused-norm input
+    wu = QWeight.quantize(torch.randn(N, K, device=DEV, generator=g) * 0.02, fmt)
+    h_ref, h = Q8Act(nb, N, DEV), Q8Act(nb, N, DEV)
+    ops.gemv_swiglu(w, wu, a, h_ref)
+    ops.gemv_norm_swiglu(w, wu, x, nw, 1e-5, h)
+    torch.testing.assert_close(h.dequantize(), h_ref.dequantize(), rtol=1e-3, atol=2e-2 * h_ref.dequantize().abs().max().item())
