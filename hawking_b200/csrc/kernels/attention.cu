@@ -45,7 +45,9 @@ __device__ __forceinline__ void load_bf16(const __nv_bfloat16* p, float (&v)[HPL
 // G query heads per KV head, HPL = head_dim / 32 dims per lane.
 template <int G, int HPL>
 __global__ void __launch_bounds__(128) attn_decode_kernel(AttnDecodeArgs a) {
-  constexpr int T = 32 / G;  // tokens per tile
+  // Tokens per tile: G*T <= 32 partial scores per butterfly; capped to bound the K/V registers.
+  constexpr int T = (32 / G) > (HPL >= 8 ? 4 : 8) ? (HPL >= 8 ? 4 : 8) : (32 / G);
+  constexpr int NV = G * T;
   constexpr int HD = HPL * 32;
   const int split = blockIdx.x, kvh = blockIdx.y, r = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -76,26 +78,35 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnDecodeArgs a) {
   const int bs = a.block_size;
   const int64_t head_stride = (int64_t)bs * HD;  // one head's slab inside a block
   for (int tt = t0 + warp * T; tt < t1; tt += 4 * T) {
-    // ---- scores for T tokens x G heads ----
-    float part[32];
+    // ---- issue the K and V loads of the whole tile up front (one round trip) ----
+    const int blk_a = btab[tt / bs];
+    const int blk_b = btab[min(tt + T - 1, t1 - 1) / bs];
+    float kreg[T][HPL], vreg[T][HPL];
 #pragma unroll
     for (int j = 0; j < T; ++j) {
       const int t = tt + j;
-      float k[HPL];
       if (t < t1) {
-        const int blk = btab[t / bs];
-        const __nv_bfloat16* kp = a.k_cache + ((int64_t)blk * a.nkv + kvh) * head_stride + (int64_t)(t % bs) * HD + lane * HPL;
-        load_bf16<HPL>(kp, k);
+        const int blk = (t / bs == tt / bs) ? blk_a : blk_b;
+        const int64_t off = ((int64_t)blk * a.nkv + kvh) * head_stride + (int64_t)(t % bs) * HD + lane * HPL;
+        load_bf16<HPL>(a.k_cache + off, kreg[j]);
+        load_bf16<HPL>(a.v_cache + off, vreg[j]);
       } else {
 #pragma unroll
-        for (int i = 0; i < HPL; ++i) k[i] = 0.f;
+        for (int i = 0; i < HPL; ++i) { kreg[j][i] = 0.f; vreg[j][i] = 0.f; }
       }
+    }
+    // ---- scores for T tokens x G heads ----
+    float part[32];
+#pragma unroll
+    for (int v = NV; v < 32; ++v) part[v] = 0.f;
+#pragma unroll
+    for (int j = 0; j < T; ++j) {
 #pragma unroll
       for (int g = 0; g < G; ++g) {
-        float s = 0.f;
+        float sdot = 0.f;
 #pragma unroll
-        for (int i = 0; i < HPL; ++i) s = fmaf(q[g][i], k[i], s);
-        part[g * T + j] = s;
+        for (int i = 0; i < HPL; ++i) sdot = fmaf(q[g][i], kreg[j][i], sdot);
+        part[g * T + j] = sdot;
       }
     }
     // Transpose-butterfly: afterwards lane L holds the full sum of value L = (g = L / T, j = L % T).
@@ -109,8 +120,8 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnDecodeArgs a) {
         part[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
       }
     }
-    const int my_g = lane / T, my_j = lane % T;
-    const float score = (tt + my_j < t1) ? part[0] : -INFINITY;
+    const int my_g = min(lane / T, G - 1), my_j = lane % T;
+    const float score = (lane < NV && tt + my_j < t1) ? part[0] : -INFINITY;
     // Per-head tile max over the T lanes of the group.
     float tmax = score;
 #pragma unroll
@@ -122,7 +133,11 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnDecodeArgs a) {
       p_new_m[g] = fmaxf(m[g], tm);
       alpha[g] = __expf(m[g] - p_new_m[g]);  // m = -inf at start gives 0
     }
-    const float p = (score == -INFINITY) ? 0.f : __expf(score - p_new_m[my_g]);
+    float mg = p_new_m[0];
+#pragma unroll
+    for (int g = 1; g < G; ++g)
+      if (my_g == g) mg = p_new_m[g];
+    const float p = (score == -INFINITY) ? 0.f : __expf(score - mg);
     float psum = p;
 #pragma unroll
     for (int o = T / 2; o > 0; o >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, o);
@@ -137,18 +152,11 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnDecodeArgs a) {
     // ---- P.V ----
 #pragma unroll
     for (int j = 0; j < T; ++j) {
-      const int t = tt + j;
-      if (t < t1) {
-        const int blk = btab[t / bs];
-        float v[HPL];
-        const __nv_bfloat16* vp = a.v_cache + ((int64_t)blk * a.nkv + kvh) * head_stride + (int64_t)(t % bs) * HD + lane * HPL;
-        load_bf16<HPL>(vp, v);
 #pragma unroll
-        for (int g = 0; g < G; ++g) {
-          const float pg = __shfl_sync(0xffffffffu, p, g * T + j);
+      for (int g = 0; g < G; ++g) {
+        const float pg = __shfl_sync(0xffffffffu, p, g * T + j);
 #pragma unroll
-          for (int i = 0; i < HPL; ++i) acc[g][i] = fmaf(pg, v[i], acc[g][i]);
-        }
+        for (int i = 0; i < HPL; ++i) acc[g][i] = fmaf(pg, vreg[j][i], acc[g][i]);
       }
     }
   }

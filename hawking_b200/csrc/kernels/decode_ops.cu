@@ -10,25 +10,42 @@
 namespace hk {
 
 // ---- RMSNorm + q8 --------------------------------------------------------------------------
+// Grid (K / 256, rows): every CTA reads the whole row (16-byte loads, all issued before the
+// reduction) to get the sum of squares, then quantises its own 256 elements (8 warps x one
+// 32-element block). One round trip to memory instead of a serial loop in a single CTA.
+constexpr int kNormSlice = 256;
 __global__ void __launch_bounds__(256) rmsnorm_q8_kernel(const float* x, int64_t x_stride, const float* w, float eps,
                                                           int norm, int K, int8_t* xq, float* xd, float* xs,
                                                           float* y) {
   __shared__ float red[32];
   pdl_wait();
-  const int r = blockIdx.x;
+  const int r = blockIdx.y;
   const float* xr = x + (int64_t)r * x_stride;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int i = blockIdx.x * kNormSlice + tid;
+  const float xv = i < K ? xr[i] : 0.f;
   float scale = 1.f;
   if (norm) {
     float ss = 0.f;
-    for (int i = threadIdx.x; i < K; i += blockDim.x) ss += xr[i] * xr[i];
+    constexpr int kV = 8;  // float4 loads per thread in flight (K <= 8192 in one pass)
+    float4 v[kV];
+#pragma unroll
+    for (int j = 0; j < kV; ++j) {
+      const int e = (tid + j * 256) * 4;
+      v[j] = e < K ? *reinterpret_cast<const float4*>(xr + e) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int j = 0; j < kV; ++j) ss += v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
+    for (int e = (tid + kV * 256) * 4; e < K; e += 1024) {
+      const float4 t = *reinterpret_cast<const float4*>(xr + e);
+      ss += t.x * t.x + t.y * t.y + t.z * t.z + t.w * t.w;
+    }
     ss = block_sum(ss, red);
     scale = rsqrtf(ss / K + eps);
   }
   pdl_launch();
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  for (int blk = warp; blk < K / 32; blk += nw) {
-    const int i = blk * 32 + lane;
-    float v = xr[i] * scale;
+  if (i < K) {  // whole warps (K % 32 == 0)
+    float v = xv * scale;
     if (w) v *= w[i];
     if (y) y[(int64_t)r * K + i] = v;
     const float amax = warp_max(fabsf(v));
@@ -37,16 +54,19 @@ __global__ void __launch_bounds__(256) rmsnorm_q8_kernel(const float* x, int64_t
     const float qsum = warp_sum((float)q);
     xq[(int64_t)r * K + i] = (int8_t)q;
     if (lane == 0) {
-      xd[(int64_t)r * (K / 32) + blk] = d;
-      xs[(int64_t)r * (K / 32) + blk] = d * qsum;
+      xd[(int64_t)r * (K / 32) + (i >> 5)] = d;
+      xs[(int64_t)r * (K / 32) + (i >> 5)] = d * qsum;
     }
   }
+  (void)warp;
 }
 
 void rmsnorm_q8_launch(const float* x, int64_t x_stride, const float* w, float eps, bool norm, int rows, int K,
                        int8_t* xq, float* xd, float* xs, float* y, cudaStream_t s, bool pdl) {
   if (K % 32) throw std::runtime_error("rmsnorm_q8: K must be a multiple of 32");
-  launch(rmsnorm_q8_kernel, dim3(rows), dim3(256), 0, s, pdl, x, x_stride, w, eps, (int)norm, K, xq, xd, xs, y);
+  if (norm && (K % 4 || x_stride % 4)) throw std::runtime_error("rmsnorm_q8: rows must be 16-byte aligned");
+  launch(rmsnorm_q8_kernel, dim3((K + kNormSlice - 1) / kNormSlice, rows), dim3(256), 0, s, pdl, x, x_stride, w, eps,
+         (int)norm, K, xq, xd, xs, y);
 }
 
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const float* x, int64_t x_stride, const float* w, float eps,

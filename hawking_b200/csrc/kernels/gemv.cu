@@ -138,8 +138,9 @@ __device__ __forceinline__ void norm_q8_to_smem(const GemvArgs& a, int nb, int8_
   __syncthreads();
 }
 
-// Kernel: one warp per row (STORE / RESID) or per gate/up row pair (SWIGLU_Q8, 32 warps).
-template <int FMT, int NB, int EPI, int XIN, int UPL>
+// Kernel: RPW rows per warp (STORE / RESID; the rows share the activation loads) or one gate/up
+// row pair per warp (SWIGLU_Q8, 32 warps).
+template <int FMT, int NB, int EPI, int XIN, int UPL, int RPW = 1>
 __global__ void __launch_bounds__(EPI == EPI_SWIGLU_Q8 ? 1024 : 256) gemv_kernel(GemvArgs a, int nb) {
   extern __shared__ __align__(16) uint8_t gsm[];
   __shared__ float red[8 * 32];
@@ -147,15 +148,19 @@ __global__ void __launch_bounds__(EPI == EPI_SWIGLU_Q8 ? 1024 : 256) gemv_kernel
   constexpr int WARPS = EPI == EPI_SWIGLU_Q8 ? 32 : 8;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_units = a.K / 128;
-  const int64_t row = (int64_t)blockIdx.x * WARPS + warp;
+  const int64_t row = ((int64_t)blockIdx.x * WARPS + warp) * RPW;
   const bool live = row < a.N;
 
   // 1) weights first (do not depend on the producer kernel)
   typename UnitOf<FMT>::T wg[UPL];
   typename UnitOf<FMT>::T wu[EPI == EPI_SWIGLU_Q8 ? UPL : 1];
+  typename UnitOf<FMT>::T w2[RPW > 1 ? UPL : 1];
   if (live) {
     load_row<FMT, UPL>(a.w0, row, n_units, wg);
     if constexpr (EPI == EPI_SWIGLU_Q8) load_row<FMT, UPL>(a.w1, row, n_units, wu);
+    if constexpr (RPW > 1) {
+      if (row + 1 < a.N) load_row<FMT, UPL>(a.w0, row + 1, n_units, w2);
+    }
   }
   pdl_wait();
 
@@ -207,18 +212,28 @@ __global__ void __launch_bounds__(EPI == EPI_SWIGLU_Q8 ? 1024 : 256) gemv_kernel
     }
   } else {
     if (!live) { pdl_launch(); return; }
-    float acc[NB];
+    float acc[NB], acc2[NB];
     row_dot_batched<FMT, NB, UPL>(wg, n_units, x, nb, acc);
+    const bool live2 = RPW > 1 && row + 1 < a.N;
+    if constexpr (RPW > 1) {
+      if (live2) row_dot_batched<FMT, NB, UPL>(w2, n_units, x, nb, acc2);
+    }
 #pragma unroll
-    for (int b = 0; b < NB; ++b) acc[b] = warp_sum(acc[b]);
+    for (int b = 0; b < NB; ++b) {
+      acc[b] = warp_sum(acc[b]);
+      if constexpr (RPW > 1) acc2[b] = live2 ? warp_sum(acc2[b]) : 0.f;
+    }
     pdl_launch();
-    if (lane < nb) {
-      float v = acc[0];
+    // lane b writes row 0 of column b; lane 16 + b writes row 1 of column b
+    const int b = lane & 15, rr = lane >> 4;
+    if (b < nb && (rr == 0 || live2)) {
+      float v = 0.f;
 #pragma unroll
-      for (int b = 1; b < NB; ++b)
-        if (lane == b) v = acc[b];
-      float* y = a.y + (int64_t)lane * a.y_stride + row;
-      if (a.bias) v += a.bias[row];
+      for (int c = 0; c < NB; ++c)
+        if (b == c) v = rr ? (RPW > 1 ? acc2[c] : 0.f) : acc[c];
+      const int64_t n = row + rr;
+      float* y = a.y + (int64_t)b * a.y_stride + n;
+      if (a.bias) v += a.bias[n];
       if constexpr (EPI == EPI_RESID) *y += v;
       else *y = v;
     }
@@ -227,7 +242,8 @@ __global__ void __launch_bounds__(EPI == EPI_SWIGLU_Q8 ? 1024 : 256) gemv_kernel
 
 template <int FMT, int EPI, int XIN, int UPL>
 static void dispatch_nb(const GemvArgs& a, int nb, cudaStream_t s, bool pdl) {
-  const int rows_per_cta = (EPI == EPI_SWIGLU_Q8) ? 32 : 8;
+  constexpr int RPW = (EPI != EPI_SWIGLU_Q8 && UPL == 1) ? 2 : 1;
+  const int rows_per_cta = (EPI == EPI_SWIGLU_Q8) ? 32 : 8 * RPW;
   const int threads = (EPI == EPI_SWIGLU_Q8) ? 1024 : 256;
   dim3 grid((a.N + rows_per_cta - 1) / rows_per_cta), block(threads);
   const size_t smem = XIN == XIN_NORM ? (size_t)nb * a.K + 2 * (size_t)nb * (a.K / 32) * 4 : 0;
@@ -235,10 +251,10 @@ static void dispatch_nb(const GemvArgs& a, int nb, cudaStream_t s, bool pdl) {
     if (smem > 48 * 1024) HK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     launch(kern, grid, block, smem, s, pdl, a, nb);
   };
-  if (nb == 1) go(gemv_kernel<FMT, 1, EPI, XIN, UPL>);
-  else if (nb == 2) go(gemv_kernel<FMT, 2, EPI, XIN, UPL>);
-  else if (nb <= 4) go(gemv_kernel<FMT, 4, EPI, XIN, UPL>);
-  else if (nb <= 8) go(gemv_kernel<FMT, 8, EPI, XIN, UPL>);
+  if (nb == 1) go(gemv_kernel<FMT, 1, EPI, XIN, UPL, RPW>);
+  else if (nb == 2) go(gemv_kernel<FMT, 2, EPI, XIN, UPL, RPW>);
+  else if (nb <= 4) go(gemv_kernel<FMT, 4, EPI, XIN, UPL, RPW>);
+  else if (nb <= 8) go(gemv_kernel<FMT, 8, EPI, XIN, UPL, RPW>);
   else throw std::runtime_error("gemv: batch columns must be 1..8");
 }
 

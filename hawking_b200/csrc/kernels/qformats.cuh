@@ -40,29 +40,35 @@ __device__ __forceinline__ void q4k_scale_min(int j, uint32_t s0, uint32_t s1, u
 }
 
 // ---- Q4_K: unit = half super-block (128 elements, 4 sub-blocks) ----------------------------
+// Planes: p0 = the raw 144-byte GGUF blocks (only the 128 quant bytes are read here), p1 = a
+// predecoded side plane per super-block of 20 bytes: d, dmin (fp16) and the eight 6-bit scales
+// and mins unpacked to bytes — the same values, laid out for word loads with no bit unpacking.
 struct UnitQ4K {
-  uint4 hdr;   // d, dmin, scales[12]
-  uint4 q[4];  // 64 bytes of qs for this half
+  uint4 q[4];     // 64 bytes of quants for this half
+  uint32_t dd;    // d | dmin << 16 (fp16 bits)
+  uint32_t sc;    // scales of sub-blocks 4h..4h+3
+  uint32_t mn;    // mins of sub-blocks 4h..4h+3
 };
 __device__ __forceinline__ void load_unit_q4k(const WPlanes& w, int64_t row, int u, UnitQ4K& r) {
-  const uint8_t* blk = w.p0 + row * w.rb0 + (int64_t)(u >> 1) * 144;
-  r.hdr = ldg_stream(blk);
-  const uint8_t* qs = blk + 16 + (u & 1) * 64;
+  const int sb = u >> 1, h = u & 1;
+  const uint8_t* qs = w.p0 + row * w.rb0 + (int64_t)sb * 144 + 16 + h * 64;
 #pragma unroll
   for (int i = 0; i < 4; ++i) r.q[i] = ldg_stream(qs + 16 * i);
+  const uint8_t* m = w.p1 + row * w.rb1 + (int64_t)sb * 20;
+  r.dd = __ldg(reinterpret_cast<const uint32_t*>(m));
+  r.sc = __ldg(reinterpret_cast<const uint32_t*>(m + 4 + 4 * h));
+  r.mn = __ldg(reinterpret_cast<const uint32_t*>(m + 12 + 4 * h));
 }
 // Dot of one unit with activation column (xq at element offset k0 = u*128).
 __device__ __forceinline__ float dot_unit_q4k(const UnitQ4K& r, int u, const int8_t* xq, const float* xd,
                                               const float* xs) {
-  const float d = __half2float(__ushort_as_half((uint16_t)(r.hdr.x & 0xFFFF)));
-  const float dmin = __half2float(__ushort_as_half((uint16_t)(r.hdr.x >> 16)));
-  const int h = u & 1;
+  const float d = __half2float(__ushort_as_half((uint16_t)(r.dd & 0xFFFF)));
+  const float dmin = __half2float(__ushort_as_half((uint16_t)(r.dd >> 16)));
   const int k0 = u * 128;
-  float acc = 0.f;
+  float acc = 0.f, mterm = 0.f;
 #pragma unroll
   for (int t = 0; t < 4; ++t) {  // sub-block 4h+t
-    int sc, mn;
-    q4k_scale_min(4 * h + t, r.hdr.y, r.hdr.z, r.hdr.w, sc, mn);
+    const int sc = (r.sc >> (8 * t)) & 0xFF, mn = (r.mn >> (8 * t)) & 0xFF;
     const uint4 qa = r.q[(t >> 1) * 2], qb = r.q[(t >> 1) * 2 + 1];
     const int shift = (t & 1) * 4;
     const int4 x0 = ldx16(xq + k0 + 32 * t), x1 = ldx16(xq + k0 + 32 * t + 16);
@@ -76,9 +82,10 @@ __device__ __forceinline__ float dot_unit_q4k(const UnitQ4K& r, int u, const int
     dot = dp4a((qb.z >> shift) & 0x0F0F0F0F, x1.z, dot);
     dot = dp4a((qb.w >> shift) & 0x0F0F0F0F, x1.w, dot);
     const int blk = (k0 >> 5) + t;
-    acc += d * (float)sc * ldxf(xd + blk) * (float)dot - dmin * (float)mn * ldxf(xs + blk);
+    acc = fmaf((float)sc * ldxf(xd + blk), (float)dot, acc);
+    mterm = fmaf((float)mn, ldxf(xs + blk), mterm);
   }
-  return acc;
+  return d * acc - dmin * mterm;
 }
 
 // ---- Q4_0 planes: unit = 4 blocks (128 elements) -------------------------------------------

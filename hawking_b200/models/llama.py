@@ -268,8 +268,9 @@ class LlamaModel:
                     ops.rmsnorm_q8(x, lw.ffn_norm, cfg.eps, self.xa.view(rows))
                     lw.moe.forward(self, rows)
                 else:
-                    self._gemv_cols(lambda c0, c1: ops.gemv_norm_swiglu(
-                        lw.w_gate, lw.w_up, x[c0:c1], lw.ffn_norm, cfg.eps, self._q8_slice(self.hq, c0, c1)), rows)
+                    ops.rmsnorm_q8(x, lw.ffn_norm, cfg.eps, self.xa.view(rows))
+                    self._gemv_cols(lambda c0, c1: ops.gemv_swiglu(lw.w_gate, lw.w_up, self.xa_view(c0, c1),
+                                                                   self._q8_slice(self.hq, c0, c1)), rows)
                     self._gemv_cols(lambda c0, c1: ops.gemv(lw.w_down,
                                                             self._q8_slice(self.hq, c0, c1, lw.w_down.K),
                                                             x[c0:c1], residual=True), rows)
@@ -286,11 +287,15 @@ class LlamaModel:
             self.logits[:nl].zero_()
             ops.tc_gemm(w.lm_head, src, self.logits[:nl], self.status, y_zeroed=True)
         else:
-            src = x
+            ops.rmsnorm_q8(x, w.out_norm, cfg.eps, self.xa.view(rows))
+            xa = self.xa
             if n_logits:
-                src = x.index_select(0, self.logit_rows[:nl].long())
-            self._gemv_cols(lambda c0, c1: ops.gemv_norm(w.lm_head, src[c0:c1], w.out_norm, cfg.eps,
-                                                         self.logits[c0:c1]), nl)
+                idx = self.logit_rows[:nl].long()
+                xa = Q8Act.__new__(Q8Act)
+                xa.K, xa.q, xa.d, xa.s = self.xa.K, self.xa.q.index_select(0, idx), \
+                    self.xa.d.index_select(0, idx), self.xa.s.index_select(0, idx)
+            self._gemv_cols(lambda c0, c1: ops.gemv(w.lm_head, self._q8_slice(xa, c0, c1, cfg.hidden),
+                                                    self.logits[c0:c1]), nl)
         if sample == "greedy":
             ops.argmax(self.logits[:nl], self.next_ids[:nl])
         elif sample == "sample":
@@ -311,11 +316,13 @@ class LlamaModel:
 
     def _attention_block_gemv(self, l, lw, rows, splits):
         x = self.x[:rows]
+        ops.rmsnorm_q8(x, lw.attn_norm, self.cfg.eps, self.xa.view(rows))
 
         def qkv_fn(c0, c1):
+            xa = self.xa_view(c0, c1)
             off = 0
             for wt in lw.wqkv:
-                ops.gemv_norm(wt, x[c0:c1], lw.attn_norm, self.cfg.eps, self.qkv[c0:c1, off:off + wt.N])
+                ops.gemv(wt, xa, self.qkv[c0:c1, off:off + wt.N])
                 off += wt.N
         self._gemv_cols(qkv_fn, rows)
         self._rope_attention(l, lw, rows, splits, out_q8=self.att.view(rows))
