@@ -175,7 +175,24 @@ __global__ void __launch_bounds__(EPI == EPI_SWIGLU_Q8 ? 1024 : 256) gemv_kernel
     norm_q8_to_smem<EPT>(a, nb, sq, sd, ss, red);
     x = XSrc{sq, sd, ss, a.K, a.K / 32};
   } else {
-    x = XSrc{a.xq, a.xd, a.xs, a.x_stride_q, a.x_stride_s};
+    // Stage the q8 activations in shared memory once per CTA (16-byte copies): every warp then
+    // reads them with LDS instead of issuing per-row global loads that throttle the LSU queue.
+    int8_t* sq = reinterpret_cast<int8_t*>(gsm);
+    float* sd = reinterpret_cast<float*>(gsm + nb * a.K);
+    float* ss = sd + nb * (a.K / 32);
+    const int nt = blockDim.x, tid = threadIdx.x;
+    const int kq16 = a.K / 16, ks = a.K / 32;
+    for (int i = tid; i < nb * kq16; i += nt) {
+      const int b = i / kq16, c = i - b * kq16;
+      reinterpret_cast<int4*>(sq)[i] = __ldg(reinterpret_cast<const int4*>(a.xq + (int64_t)b * a.x_stride_q) + c);
+    }
+    for (int i = tid; i < nb * ks; i += nt) {
+      const int b = i / ks, c = i - b * ks;
+      sd[i] = __ldg(a.xd + (int64_t)b * a.x_stride_s + c);
+      ss[i] = __ldg(a.xs + (int64_t)b * a.x_stride_s + c);
+    }
+    __syncthreads();
+    x = XSrc{sq, sd, ss, a.K, ks};
   }
 
   // 3) dot products + epilogue
@@ -246,7 +263,7 @@ static void dispatch_nb(const GemvArgs& a, int nb, cudaStream_t s, bool pdl) {
   const int rows_per_cta = (EPI == EPI_SWIGLU_Q8) ? 32 : 8 * RPW;
   const int threads = (EPI == EPI_SWIGLU_Q8) ? 1024 : 256;
   dim3 grid((a.N + rows_per_cta - 1) / rows_per_cta), block(threads);
-  const size_t smem = XIN == XIN_NORM ? (size_t)nb * a.K + 2 * (size_t)nb * (a.K / 32) * 4 : 0;
+  const size_t smem = (size_t)nb * a.K + 2 * (size_t)nb * (a.K / 32) * 4;  // q8 activations staged in smem
   auto go = [&](auto kern) {
     if (smem > 48 * 1024) HK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     launch(kern, grid, block, smem, s, pdl, a, nb);
