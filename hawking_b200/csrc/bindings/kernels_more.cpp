@@ -23,8 +23,11 @@ void quantize(int64_t fmt, const Tensor& x, const std::vector<Tensor>& planes) {
   const c10::cuda::CUDAGuard g(x.device());
   hk::quantize_launch((int)fmt, x.data_ptr<float>(), x.numel(), p[0], p[1], p[2], p[3], cur_stream());
 }
-void tc_gemm(int64_t fmt, const Tensor& w, int64_t N, int64_t K, const Tensor& x, const Tensor& y, bool atomic,
-             bool y_zeroed, int64_t k_splits, int64_t bn, const Tensor& status, bool pdl) {
+void tc_gemm(int64_t fmt, const std::vector<Tensor>& planes, int64_t N, int64_t K, const Tensor& x, const Tensor& y,
+             bool atomic, bool y_zeroed, int64_t k_splits, int64_t bn, const Tensor& status, bool pdl) {
+  TORCH_CHECK(planes.size() == 2, "tc_gemm: Q4_K expects [quants, headers] planes");
+  const Tensor& w = planes[0];
+  const Tensor& wh = planes[1];
   TORCH_CHECK(w.is_cuda() && x.is_cuda() && y.is_cuda(), "tc_gemm: CUDA tensors required");
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.stride(-1) == 1, "tc_gemm: x must be bf16 rows");
   TORCH_CHECK(y.scalar_type() == at::kFloat && y.stride(-1) == 1, "tc_gemm: y must be fp32 rows");
@@ -34,6 +37,8 @@ void tc_gemm(int64_t fmt, const Tensor& w, int64_t N, int64_t K, const Tensor& x
   g.fmt = (int)fmt;
   g.w = reinterpret_cast<const uint8_t*>(w.data_ptr());
   g.w_row_bytes = w.stride(0);
+  g.w_hdr = reinterpret_cast<const uint8_t*>(wh.data_ptr());
+  g.w_hdr_row_bytes = wh.stride(0);
   g.N = (int)N;
   g.K = (int)K;
   g.x = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
@@ -157,7 +162,7 @@ void moe_gemv(int64_t fmt, int64_t epi, const std::vector<Tensor>& w0, const std
 namespace hk {
 void register_more_kernels(py::module_& m) {
   m.def("quantize", &quantize, py::arg("fmt"), py::arg("x"), py::arg("planes"));
-  m.def("tc_gemm", &tc_gemm, py::arg("fmt"), py::arg("w"), py::arg("N"), py::arg("K"), py::arg("x"), py::arg("y"),
+  m.def("tc_gemm", &tc_gemm, py::arg("fmt"), py::arg("planes"), py::arg("N"), py::arg("K"), py::arg("x"), py::arg("y"),
         py::arg("atomic"), py::arg("y_zeroed"), py::arg("k_splits"), py::arg("bn"), py::arg("status"),
         py::arg("pdl") = false);
   m.def("tc_gemm_splits", &hk::tc_gemm_splits);

@@ -137,8 +137,10 @@ void embed_launch(int fmt, const WPlanes& table, const int* ids, int R, int H, f
 // ---- tensor-core dequant GEMM (gemm_tc.cu) ----
 struct TcGemmArgs {
   int fmt;                      // weight format (Q4_K)
-  const uint8_t* w;             // raw blocks [N, w_row_bytes]
+  const uint8_t* w;             // quants plane [N, w_row_bytes] (K/2 bytes per row)
   int64_t w_row_bytes;
+  const uint8_t* w_hdr;         // header plane [N, w_hdr_row_bytes] (16 bytes per super-block)
+  int64_t w_hdr_row_bytes;
   int N, K;
   const __nv_bfloat16* x;       // [M, x_stride] bf16
   int64_t x_stride;

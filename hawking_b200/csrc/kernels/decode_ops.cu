@@ -426,16 +426,16 @@ __device__ __forceinline__ float dequant_elem(int fmt, const WPlanes& t, int64_t
       const int q = ((j & 16) ? (b >> 4) : (b & 0xF)) | (((qh >> j) & 1) << 4);
       return __half2float(reinterpret_cast<const __half*>(t.p1 + row * t.rb1)[k >> 5]) * (q - 16);
     }
-    case WF_Q4_K: {
-      const uint8_t* blk = t.p0 + row * t.rb0 + (int64_t)(k >> 8) * 144;
+    case WF_Q4_K: {  // planes: quants [N, K/2], headers [N, K/256 * 16]
+      const uint8_t* hdr = t.p1 + row * t.rb1 + (int64_t)(k >> 8) * 16;
       const int e = k & 255, j = e >> 5;  // sub-block
-      const uint32_t* s = reinterpret_cast<const uint32_t*>(blk + 4);
+      const uint32_t* s = reinterpret_cast<const uint32_t*>(hdr + 4);
       int sc, mn;
       q4k_scale_min(j, s[0], s[1], s[2], sc, mn);
-      const uint8_t qb = blk[16 + (j >> 1) * 32 + (e & 31)];
+      const uint8_t qb = (t.p0 + row * t.rb0 + (int64_t)(k >> 8) * 128)[(j >> 1) * 32 + (e & 31)];
       const int q = (j & 1) ? (qb >> 4) : (qb & 0xF);
-      const float d = __half2float(reinterpret_cast<const __half*>(blk)[0]);
-      const float dmin = __half2float(reinterpret_cast<const __half*>(blk)[1]);
+      const float d = __half2float(reinterpret_cast<const __half*>(hdr)[0]);
+      const float dmin = __half2float(reinterpret_cast<const __half*>(hdr)[1]);
       return d * sc * q - dmin * mn;
     }
     case WF_Q6_K: {

@@ -3,7 +3,8 @@
 //
 // One CTA owns a 128-row weight tile and a BN-token tile over a K range (split-K across
 // blockIdx.z, reduced with fp32 atomics). Warp roles:
-//   warp 0      TMA producer of raw Q4_K bytes (header 16 B + 64 B of quants per row per stage)
+//   warp 0      TMA producer of the Q4_K bytes (16-byte header + 64 quant bytes per row per stage,
+//               from the header and quants planes)
 //   warp 1      TMA producer of the bf16 activation tile (128-byte swizzle, two 64-wide atoms)
 //   warp 2      TMEM allocation and the single-thread UMMA issuer
 //   warps 4-11  dequantisers: raw smem -> bf16 A tile in the canonical K-major SW128 layout
@@ -130,8 +131,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(&raw_empty[slot], ((i / DR) & 1) ^ 1, a.status)) break;
         const int gs = s0 + i, sb = gs >> 1, h = gs & 1;
         mbar_arrive_expect_tx(&raw_full[slot], RAW_HDR + RAW_QS);
-        tma_load_2d(smem + L::off_hdr + slot * RAW_HDR, &tm_hdr, sb * 144, n0, &raw_full[slot]);
-        tma_load_2d(smem + L::off_qs + slot * RAW_QS, &tm_qs, sb * 144 + 16 + 64 * h, n0, &raw_full[slot]);
+        tma_load_2d(smem + L::off_hdr + slot * RAW_HDR, &tm_hdr, sb * 16, n0, &raw_full[slot]);
+        tma_load_2d(smem + L::off_qs + slot * RAW_QS, &tm_qs, (2 * sb + h) * 64, n0, &raw_full[slot]);
         ++issued;
       }
       // Drain: every issued copy has landed before the CTA may exit.
@@ -283,8 +284,8 @@ CUtensorMap make_map_2d(CUtensorMapDataType dt, const void* base, uint64_t inner
 template <int BN>
 void launch_bn(const TcGemmArgs& g, cudaStream_t s) {
   using L = Layout<BN>;
-  const uint64_t rb = (uint64_t)g.w_row_bytes;
-  CUtensorMap tm_hdr = make_map_2d(CU_TENSOR_MAP_DATA_TYPE_UINT8, g.w, rb, g.N, rb, 16, BM, CU_TENSOR_MAP_SWIZZLE_NONE);
+  const uint64_t rb = (uint64_t)g.w_row_bytes, hb = (uint64_t)g.w_hdr_row_bytes;
+  CUtensorMap tm_hdr = make_map_2d(CU_TENSOR_MAP_DATA_TYPE_UINT8, g.w_hdr, hb, g.N, hb, 16, BM, CU_TENSOR_MAP_SWIZZLE_NONE);
   CUtensorMap tm_qs = make_map_2d(CU_TENSOR_MAP_DATA_TYPE_UINT8, g.w, rb, g.N, rb, 64, BM, CU_TENSOR_MAP_SWIZZLE_NONE);
   CUtensorMap tm_x = make_map_2d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, g.x, g.K, g.M, (uint64_t)g.x_stride * 2, 64, BN,
                                  CU_TENSOR_MAP_SWIZZLE_128B);

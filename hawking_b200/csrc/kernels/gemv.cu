@@ -18,33 +18,50 @@
 
 namespace hk {
 
-template <int FMT> struct UnitOf;
-template <> struct UnitOf<WF_Q4_K> { using T = UnitQ4K; };
-template <> struct UnitOf<WF_Q4_0> { using T = UnitQ4_0; };
-template <> struct UnitOf<WF_Q8_0> { using T = UnitQ8_0; };
-template <> struct UnitOf<WF_Q5_0> { using T = UnitQ5_0; };
-template <> struct UnitOf<WF_Q6_K> { using T = UnitQ6K; };
-
-template <int FMT>
-__device__ __forceinline__ void load_unit(const WPlanes& w, int64_t row, int u, typename UnitOf<FMT>::T& r) {
-  if constexpr (FMT == WF_Q4_K) load_unit_q4k(w, row, u, r);
-  else if constexpr (FMT == WF_Q4_0) load_unit_q4_0(w, row, u, r);
-  else if constexpr (FMT == WF_Q8_0) load_unit_q8_0(w, row, u, r);
-  else if constexpr (FMT == WF_Q5_0) load_unit_q5_0(w, row, u, r);
-  else load_unit_q6k(w, row, u, r);
-}
-template <int FMT>
-__device__ __forceinline__ float dot_unit(const typename UnitOf<FMT>::T& r, int u, const int8_t* xq,
-                                          const float* xd, const float* xs) {
-  if constexpr (FMT == WF_Q4_K) return dot_unit_q4k(r, u, xq, xd, xs);
-  else if constexpr (FMT == WF_Q4_0) return dot_unit_q4_0(r, u, xq, xd, xs);
-  else if constexpr (FMT == WF_Q8_0) return dot_unit_q8_0(r, u, xq, xd, xs);
-  else if constexpr (FMT == WF_Q5_0) return dot_unit_q5_0(r, u, xq, xd, xs);
-  else return dot_unit_q6k(r, u, xq, xd, xs);
-}
-
-// Units (128 elements) per lane: 1 covers K <= 4096 with one batch of loads, 4 covers K <= 16384.
-constexpr int kMaxUnitsPerLane = 4;
+// Format traits: the per-lane work item ("unit") and how many a lane loads per round. Q4_K /
+// Q8_0 / Q4_0 use the coalesced chunk mapping (lane L owns units L + 32 i, adjacent lanes read
+// adjacent bytes); Q6_K / Q5_0 use 128-element units.
+template <int FMT> struct Fmt;
+template <> struct Fmt<WF_Q4_K> {
+  using T = ChunkQ4K;
+  static constexpr int ELEMS = 64, UPL = 2;
+  static __device__ __forceinline__ void load(const WPlanes& w, int64_t r, int c, T& u) { load_chunk_q4k(w, r, c, u); }
+  static __device__ __forceinline__ float dot(const T& u, int c, const int8_t* q, const float* d, const float* s) {
+    return dot_chunk_q4k(u, c, q, d, s);
+  }
+};
+template <> struct Fmt<WF_Q8_0> {
+  using T = ChunkQ8_0;
+  static constexpr int ELEMS = 32, UPL = 4;
+  static __device__ __forceinline__ void load(const WPlanes& w, int64_t r, int c, T& u) { load_chunk_q8_0(w, r, c, u); }
+  static __device__ __forceinline__ float dot(const T& u, int c, const int8_t* q, const float* d, const float* s) {
+    return dot_chunk_q8_0(u, c, q, d, s);
+  }
+};
+template <> struct Fmt<WF_Q4_0> {
+  using T = ChunkQ4_0;
+  static constexpr int ELEMS = 32, UPL = 4;
+  static __device__ __forceinline__ void load(const WPlanes& w, int64_t r, int c, T& u) { load_chunk_q4_0(w, r, c, u); }
+  static __device__ __forceinline__ float dot(const T& u, int c, const int8_t* q, const float* d, const float* s) {
+    return dot_chunk_q4_0(u, c, q, d, s);
+  }
+};
+template <> struct Fmt<WF_Q6_K> {
+  using T = UnitQ6K;
+  static constexpr int ELEMS = 128, UPL = 1;
+  static __device__ __forceinline__ void load(const WPlanes& w, int64_t r, int c, T& u) { load_unit_q6k(w, r, c, u); }
+  static __device__ __forceinline__ float dot(const T& u, int c, const int8_t* q, const float* d, const float* s) {
+    return dot_unit_q6k(u, c, q, d, s);
+  }
+};
+template <> struct Fmt<WF_Q5_0> {
+  using T = UnitQ5_0;
+  static constexpr int ELEMS = 128, UPL = 1;
+  static __device__ __forceinline__ void load(const WPlanes& w, int64_t r, int c, T& u) { load_unit_q5_0(w, r, c, u); }
+  static __device__ __forceinline__ float dot(const T& u, int c, const int8_t* q, const float* d, const float* s) {
+    return dot_unit_q5_0(u, c, q, d, s);
+  }
+};
 
 // The activation source of one launch, resolved to plain pointers (global or shared memory).
 struct XSrc {
@@ -54,34 +71,46 @@ struct XSrc {
   int64_t sq, ss;  // per-column strides
 };
 
-// Row dot over NB columns with all of the lane's weight units loaded up front (u = lane + 32 j).
-template <int FMT, int NB, int UPL>
-__device__ __forceinline__ void row_dot_batched(typename UnitOf<FMT>::T (&r)[UPL], int n_units,
-                                                const XSrc& x, int nb, float (&acc)[NB]) {
+// One round: up to UPL units per lane (u = base + lane + 32 j).
+template <int FMT>
+__device__ __forceinline__ void load_round(const WPlanes& w, int64_t row, int base, int n_units,
+                                           typename Fmt<FMT>::T (&r)[Fmt<FMT>::UPL]) {
   const int lane = threadIdx.x & 31;
 #pragma unroll
-  for (int b = 0; b < NB; ++b) acc[b] = 0.f;
+  for (int j = 0; j < Fmt<FMT>::UPL; ++j) {
+    const int u = base + lane + 32 * j;
+    if (u < n_units) Fmt<FMT>::load(w, row, u, r[j]);
+  }
+}
+template <int FMT, int NB>
+__device__ __forceinline__ void dot_round(const typename Fmt<FMT>::T (&r)[Fmt<FMT>::UPL], int base, int n_units,
+                                          const XSrc& x, int nb, float (&acc)[NB]) {
+  const int lane = threadIdx.x & 31;
 #pragma unroll
-  for (int j = 0; j < UPL; ++j) {
-    const int u = lane + 32 * j;
+  for (int j = 0; j < Fmt<FMT>::UPL; ++j) {
+    const int u = base + lane + 32 * j;
     if (u < n_units) {
 #pragma unroll
       for (int b = 0; b < NB; ++b) {
         const int bb = b < nb ? b : 0;  // padded columns recompute column 0 and are discarded
-        acc[b] += dot_unit<FMT>(r[j], u, x.q + bb * x.sq, x.d + bb * x.ss, x.s + bb * x.ss);
+        acc[b] += Fmt<FMT>::dot(r[j], u, x.q + bb * x.sq, x.d + bb * x.ss, x.s + bb * x.ss);
       }
     }
   }
 }
-
-template <int FMT, int UPL>
-__device__ __forceinline__ void load_row(const WPlanes& w, int64_t row, int n_units,
-                                         typename UnitOf<FMT>::T (&r)[UPL]) {
-  const int lane = threadIdx.x & 31;
+// Full row dot: the first round was loaded by the caller (before the PDL wait), the rest stream.
+template <int FMT, int NB>
+__device__ __forceinline__ void row_dot(const WPlanes& w, int64_t row, int n_units,
+                                        typename Fmt<FMT>::T (&first)[Fmt<FMT>::UPL], const XSrc& x, int nb,
+                                        float (&acc)[NB]) {
 #pragma unroll
-  for (int j = 0; j < UPL; ++j) {
-    const int u = lane + 32 * j;
-    if (u < n_units) load_unit<FMT>(w, row, u, r[j]);
+  for (int b = 0; b < NB; ++b) acc[b] = 0.f;
+  constexpr int STEP = 32 * Fmt<FMT>::UPL;
+  dot_round<FMT, NB>(first, 0, n_units, x, nb, acc);
+  for (int base = STEP; base < n_units; base += STEP) {
+    typename Fmt<FMT>::T r[Fmt<FMT>::UPL];
+    load_round<FMT>(w, row, base, n_units, r);
+    dot_round<FMT, NB>(r, base, n_units, x, nb, acc);
   }
 }
 
@@ -138,69 +167,62 @@ __device__ __forceinline__ void norm_q8_to_smem(const GemvArgs& a, int nb, int8_
   __syncthreads();
 }
 
-// Kernel: RPW rows per warp (STORE / RESID; the rows share the activation loads) or one gate/up
-// row pair per warp (SWIGLU_Q8, 32 warps).
-template <int FMT, int NB, int EPI, int XIN, int UPL, int RPW = 1>
+// Kernel: one warp per row (STORE / RESID), or one gate/up row pair per warp (SWIGLU_Q8, 32
+// warps so the CTA's 32 rows form one q8 block of the output).
+template <int FMT, int NB, int EPI, int XIN>
 __global__ void __launch_bounds__(EPI == EPI_SWIGLU_Q8 ? 1024 : 256) gemv_kernel(GemvArgs a, int nb) {
   extern __shared__ __align__(16) uint8_t gsm[];
   __shared__ float red[8 * 32];
   __shared__ float hbuf[NB][32];
   constexpr int WARPS = EPI == EPI_SWIGLU_Q8 ? 32 : 8;
+  constexpr int UPL = Fmt<FMT>::UPL;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_units = a.K / 128;
-  const int64_t row = ((int64_t)blockIdx.x * WARPS + warp) * RPW;
+  const int n_units = a.K / Fmt<FMT>::ELEMS;
+  const int64_t row = (int64_t)blockIdx.x * WARPS + warp;
   const bool live = row < a.N;
 
-  // 1) weights first (do not depend on the producer kernel)
-  typename UnitOf<FMT>::T wg[UPL];
-  typename UnitOf<FMT>::T wu[EPI == EPI_SWIGLU_Q8 ? UPL : 1];
-  typename UnitOf<FMT>::T w2[RPW > 1 ? UPL : 1];
+  // 1) first round of weights (independent of the producer kernel)
+  typename Fmt<FMT>::T wg[UPL];
+  typename Fmt<FMT>::T wu[EPI == EPI_SWIGLU_Q8 ? UPL : 1];
   if (live) {
-    load_row<FMT, UPL>(a.w0, row, n_units, wg);
-    if constexpr (EPI == EPI_SWIGLU_Q8) load_row<FMT, UPL>(a.w1, row, n_units, wu);
-    if constexpr (RPW > 1) {
-      if (row + 1 < a.N) load_row<FMT, UPL>(a.w0, row + 1, n_units, w2);
-    }
+    load_round<FMT>(a.w0, row, 0, n_units, wg);
+    if constexpr (EPI == EPI_SWIGLU_Q8) load_round<FMT>(a.w1, row, 0, n_units, wu);
   }
   pdl_wait();
 
-  // 2) activations
+  // 2) activations into shared memory
   XSrc x;
-  if constexpr (XIN == XIN_NORM) {
+  {
     int8_t* sq = reinterpret_cast<int8_t*>(gsm);
     float* sd = reinterpret_cast<float*>(gsm + nb * a.K);
     float* ss = sd + nb * (a.K / 32);
-    constexpr int NT = WARPS * 32;
-    constexpr int EPT = (4096 + NT - 1) / NT;  // elements per thread, K <= 4096 on this path
-    norm_q8_to_smem<EPT>(a, nb, sq, sd, ss, red);
+    if constexpr (XIN == XIN_NORM) {
+      constexpr int NT = WARPS * 32;
+      constexpr int EPT = (4096 + NT - 1) / NT;
+      norm_q8_to_smem<EPT>(a, nb, sq, sd, ss, red);
+    } else {
+      const int nt = blockDim.x, tid = threadIdx.x;
+      const int kq16 = a.K / 16, ks = a.K / 32;
+      for (int i = tid; i < nb * kq16; i += nt) {
+        const int b = i / kq16, c = i - b * kq16;
+        reinterpret_cast<int4*>(sq)[i] = __ldg(reinterpret_cast<const int4*>(a.xq + (int64_t)b * a.x_stride_q) + c);
+      }
+      for (int i = tid; i < nb * ks; i += nt) {
+        const int b = i / ks, c = i - b * ks;
+        sd[i] = __ldg(a.xd + (int64_t)b * a.x_stride_s + c);
+        ss[i] = __ldg(a.xs + (int64_t)b * a.x_stride_s + c);
+      }
+      __syncthreads();
+    }
     x = XSrc{sq, sd, ss, a.K, a.K / 32};
-  } else {
-    // Stage the q8 activations in shared memory once per CTA (16-byte copies): every warp then
-    // reads them with LDS instead of issuing per-row global loads that throttle the LSU queue.
-    int8_t* sq = reinterpret_cast<int8_t*>(gsm);
-    float* sd = reinterpret_cast<float*>(gsm + nb * a.K);
-    float* ss = sd + nb * (a.K / 32);
-    const int nt = blockDim.x, tid = threadIdx.x;
-    const int kq16 = a.K / 16, ks = a.K / 32;
-    for (int i = tid; i < nb * kq16; i += nt) {
-      const int b = i / kq16, c = i - b * kq16;
-      reinterpret_cast<int4*>(sq)[i] = __ldg(reinterpret_cast<const int4*>(a.xq + (int64_t)b * a.x_stride_q) + c);
-    }
-    for (int i = tid; i < nb * ks; i += nt) {
-      const int b = i / ks, c = i - b * ks;
-      sd[i] = __ldg(a.xd + (int64_t)b * a.x_stride_s + c);
-      ss[i] = __ldg(a.xs + (int64_t)b * a.x_stride_s + c);
-    }
-    __syncthreads();
-    x = XSrc{sq, sd, ss, a.K, ks};
   }
 
   // 3) dot products + epilogue
   if constexpr (EPI == EPI_SWIGLU_Q8) {
     float g[NB], u[NB];
     if (live) {
-      row_dot_batched<FMT, NB, UPL>(wg, n_units, x, nb, g);
-      row_dot_batched<FMT, NB, UPL>(wu, n_units, x, nb, u);
+      row_dot<FMT, NB>(a.w0, row, n_units, wg, x, nb, g);
+      row_dot<FMT, NB>(a.w1, row, n_units, wu, x, nb, u);
     }
 #pragma unroll
     for (int b = 0; b < NB; ++b) {
@@ -229,38 +251,27 @@ __global__ void __launch_bounds__(EPI == EPI_SWIGLU_Q8 ? 1024 : 256) gemv_kernel
     }
   } else {
     if (!live) { pdl_launch(); return; }
-    float acc[NB], acc2[NB];
-    row_dot_batched<FMT, NB, UPL>(wg, n_units, x, nb, acc);
-    const bool live2 = RPW > 1 && row + 1 < a.N;
-    if constexpr (RPW > 1) {
-      if (live2) row_dot_batched<FMT, NB, UPL>(w2, n_units, x, nb, acc2);
-    }
+    float acc[NB];
+    row_dot<FMT, NB>(a.w0, row, n_units, wg, x, nb, acc);
 #pragma unroll
-    for (int b = 0; b < NB; ++b) {
-      acc[b] = warp_sum(acc[b]);
-      if constexpr (RPW > 1) acc2[b] = live2 ? warp_sum(acc2[b]) : 0.f;
-    }
+    for (int b = 0; b < NB; ++b) acc[b] = warp_sum(acc[b]);
     pdl_launch();
-    // lane b writes row 0 of column b; lane 16 + b writes row 1 of column b
-    const int b = lane & 15, rr = lane >> 4;
-    if (b < nb && (rr == 0 || live2)) {
-      float v = 0.f;
+    if (lane < nb) {
+      float v = acc[0];
 #pragma unroll
-      for (int c = 0; c < NB; ++c)
-        if (b == c) v = rr ? (RPW > 1 ? acc2[c] : 0.f) : acc[c];
-      const int64_t n = row + rr;
-      float* y = a.y + (int64_t)b * a.y_stride + n;
-      if (a.bias) v += a.bias[n];
+      for (int c = 1; c < NB; ++c)
+        if (lane == c) v = acc[c];
+      float* y = a.y + (int64_t)lane * a.y_stride + row;
+      if (a.bias) v += a.bias[row];
       if constexpr (EPI == EPI_RESID) *y += v;
       else *y = v;
     }
   }
 }
 
-template <int FMT, int EPI, int XIN, int UPL>
+template <int FMT, int EPI, int XIN>
 static void dispatch_nb(const GemvArgs& a, int nb, cudaStream_t s, bool pdl) {
-  constexpr int RPW = (EPI != EPI_SWIGLU_Q8 && UPL == 1) ? 2 : 1;
-  const int rows_per_cta = (EPI == EPI_SWIGLU_Q8) ? 32 : 8 * RPW;
+  const int rows_per_cta = (EPI == EPI_SWIGLU_Q8) ? 32 : 8;
   const int threads = (EPI == EPI_SWIGLU_Q8) ? 1024 : 256;
   dim3 grid((a.N + rows_per_cta - 1) / rows_per_cta), block(threads);
   const size_t smem = (size_t)nb * a.K + 2 * (size_t)nb * (a.K / 32) * 4;  // q8 activations staged in smem
@@ -268,21 +279,21 @@ static void dispatch_nb(const GemvArgs& a, int nb, cudaStream_t s, bool pdl) {
     if (smem > 48 * 1024) HK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     launch(kern, grid, block, smem, s, pdl, a, nb);
   };
-  if (nb == 1) go(gemv_kernel<FMT, 1, EPI, XIN, UPL, RPW>);
-  else if (nb == 2) go(gemv_kernel<FMT, 2, EPI, XIN, UPL, RPW>);
-  else if (nb <= 4) go(gemv_kernel<FMT, 4, EPI, XIN, UPL, RPW>);
-  else if (nb <= 8) go(gemv_kernel<FMT, 8, EPI, XIN, UPL, RPW>);
+  if (nb == 1) go(gemv_kernel<FMT, 1, EPI, XIN>);
+  else if (nb == 2) go(gemv_kernel<FMT, 2, EPI, XIN>);
+  else if (nb <= 4) go(gemv_kernel<FMT, 4, EPI, XIN>);
+  else if (nb <= 8) go(gemv_kernel<FMT, 8, EPI, XIN>);
   else throw std::runtime_error("gemv: batch columns must be 1..8");
 }
 
-template <int EPI, int XIN, int UPL>
+template <int EPI, int XIN>
 static void dispatch_fmt(int fmt, const GemvArgs& a, int nb, cudaStream_t s, bool pdl) {
   switch (fmt) {
-    case WF_Q4_K: dispatch_nb<WF_Q4_K, EPI, XIN, UPL>(a, nb, s, pdl); break;
-    case WF_Q4_0: dispatch_nb<WF_Q4_0, EPI, XIN, UPL>(a, nb, s, pdl); break;
-    case WF_Q8_0: dispatch_nb<WF_Q8_0, EPI, XIN, UPL>(a, nb, s, pdl); break;
-    case WF_Q5_0: dispatch_nb<WF_Q5_0, EPI, XIN, UPL>(a, nb, s, pdl); break;
-    case WF_Q6_K: dispatch_nb<WF_Q6_K, EPI, XIN, UPL>(a, nb, s, pdl); break;
+    case WF_Q4_K: dispatch_nb<WF_Q4_K, EPI, XIN>(a, nb, s, pdl); break;
+    case WF_Q4_0: dispatch_nb<WF_Q4_0, EPI, XIN>(a, nb, s, pdl); break;
+    case WF_Q8_0: dispatch_nb<WF_Q8_0, EPI, XIN>(a, nb, s, pdl); break;
+    case WF_Q5_0: dispatch_nb<WF_Q5_0, EPI, XIN>(a, nb, s, pdl); break;
+    case WF_Q6_K: dispatch_nb<WF_Q6_K, EPI, XIN>(a, nb, s, pdl); break;
     default: throw std::runtime_error("gemv: unsupported weight format " + std::to_string(fmt));
   }
 }
@@ -290,29 +301,19 @@ static void dispatch_fmt(int fmt, const GemvArgs& a, int nb, cudaStream_t s, boo
 void gemv_launch(int fmt, int epi, const GemvArgs& a, int nb, cudaStream_t s, bool pdl) {
   if (a.K % 128) throw std::runtime_error("gemv: K must be a multiple of 128");
   if ((fmt == WF_Q4_K || fmt == WF_Q6_K) && a.K % 256) throw std::runtime_error("gemv: K-quant rows need K % 256 == 0");
-  if (a.K > kMaxUnitsPerLane * 32 * 128) throw std::runtime_error("gemv: K too large");
-  const bool small_k = a.K <= 32 * 128;
+  if (a.K > 65536) throw std::runtime_error("gemv: K too large for the shared activation buffer");
   if (epi == EPI_SWIGLU_Q8 && a.N % 32) throw std::runtime_error("gemv swiglu: N must be a multiple of 32");
   if (a.x_f32) {  // fused RMSNorm -> q8 prologue (K <= 4096)
-    if (!small_k) throw std::runtime_error("gemv: the fused-norm input path needs K <= 4096");
-    if (epi == EPI_STORE) dispatch_fmt<EPI_STORE, XIN_NORM, 1>(fmt, a, nb, s, pdl);
-    else if (epi == EPI_SWIGLU_Q8) dispatch_fmt<EPI_SWIGLU_Q8, XIN_NORM, 1>(fmt, a, nb, s, pdl);
+    if (a.K > 4096) throw std::runtime_error("gemv: the fused-norm input path needs K <= 4096");
+    if (epi == EPI_STORE) dispatch_fmt<EPI_STORE, XIN_NORM>(fmt, a, nb, s, pdl);
+    else if (epi == EPI_SWIGLU_Q8) dispatch_fmt<EPI_SWIGLU_Q8, XIN_NORM>(fmt, a, nb, s, pdl);
     else throw std::runtime_error("gemv: fused-norm input supports STORE and SWIGLU_Q8");
     return;
   }
   switch (epi) {
-    case EPI_STORE:
-      if (small_k) dispatch_fmt<EPI_STORE, XIN_Q8, 1>(fmt, a, nb, s, pdl);
-      else dispatch_fmt<EPI_STORE, XIN_Q8, 4>(fmt, a, nb, s, pdl);
-      break;
-    case EPI_RESID:
-      if (small_k) dispatch_fmt<EPI_RESID, XIN_Q8, 1>(fmt, a, nb, s, pdl);
-      else dispatch_fmt<EPI_RESID, XIN_Q8, 4>(fmt, a, nb, s, pdl);
-      break;
-    case EPI_SWIGLU_Q8:
-      if (!small_k) throw std::runtime_error("gemv swiglu: K <= 4096");
-      dispatch_fmt<EPI_SWIGLU_Q8, XIN_Q8, 1>(fmt, a, nb, s, pdl);
-      break;
+    case EPI_STORE: dispatch_fmt<EPI_STORE, XIN_Q8>(fmt, a, nb, s, pdl); break;
+    case EPI_RESID: dispatch_fmt<EPI_RESID, XIN_Q8>(fmt, a, nb, s, pdl); break;
+    case EPI_SWIGLU_Q8: dispatch_fmt<EPI_SWIGLU_Q8, XIN_Q8>(fmt, a, nb, s, pdl); break;
     default: throw std::runtime_error("gemv: bad epilogue");
   }
 }

@@ -39,36 +39,32 @@ __device__ __forceinline__ void q4k_scale_min(int j, uint32_t s0, uint32_t s1, u
   }
 }
 
-// ---- Q4_K: unit = half super-block (128 elements, 4 sub-blocks) ----------------------------
-// Planes: p0 = the raw 144-byte GGUF blocks (only the 128 quant bytes are read here), p1 = a
-// predecoded side plane per super-block of 20 bytes: d, dmin (fp16) and the eight 6-bit scales
-// and mins unpacked to bytes — the same values, laid out for word loads with no bit unpacking.
+// ---- Q4_K planes ------------------------------------------------------------------------------
+// p0 = quants [N, K/2] (the 128 quant bytes of every super-block, in order), p1 = headers
+// [N, K/256 * 16] (d, dmin, 12 packed scale bytes). Together exactly the GGUF block bytes.
+//
+// Unit (legacy per-lane mapping, used by the grouped MoE GEMV): half a super-block, 128 elements.
 struct UnitQ4K {
-  uint4 q[4];     // 64 bytes of quants for this half
-  uint32_t dd;    // d | dmin << 16 (fp16 bits)
-  uint32_t sc;    // scales of sub-blocks 4h..4h+3
-  uint32_t mn;    // mins of sub-blocks 4h..4h+3
+  uint4 hdr;   // d, dmin, scales[12]
+  uint4 q[4];  // 64 bytes of qs for this half
 };
 __device__ __forceinline__ void load_unit_q4k(const WPlanes& w, int64_t row, int u, UnitQ4K& r) {
-  const int sb = u >> 1, h = u & 1;
-  const uint8_t* qs = w.p0 + row * w.rb0 + (int64_t)sb * 144 + 16 + h * 64;
+  r.hdr = __ldg(reinterpret_cast<const uint4*>(w.p1 + row * w.rb1 + (int64_t)(u >> 1) * 16));
+  const uint8_t* qs = w.p0 + row * w.rb0 + (int64_t)u * 64;
 #pragma unroll
   for (int i = 0; i < 4; ++i) r.q[i] = ldg_stream(qs + 16 * i);
-  const uint8_t* m = w.p1 + row * w.rb1 + (int64_t)sb * 20;
-  r.dd = __ldg(reinterpret_cast<const uint32_t*>(m));
-  r.sc = __ldg(reinterpret_cast<const uint32_t*>(m + 4 + 4 * h));
-  r.mn = __ldg(reinterpret_cast<const uint32_t*>(m + 12 + 4 * h));
 }
-// Dot of one unit with activation column (xq at element offset k0 = u*128).
 __device__ __forceinline__ float dot_unit_q4k(const UnitQ4K& r, int u, const int8_t* xq, const float* xd,
                                               const float* xs) {
-  const float d = __half2float(__ushort_as_half((uint16_t)(r.dd & 0xFFFF)));
-  const float dmin = __half2float(__ushort_as_half((uint16_t)(r.dd >> 16)));
+  const float d = __half2float(__ushort_as_half((uint16_t)(r.hdr.x & 0xFFFF)));
+  const float dmin = __half2float(__ushort_as_half((uint16_t)(r.hdr.x >> 16)));
+  const int h = u & 1;
   const int k0 = u * 128;
-  float acc = 0.f, mterm = 0.f;
+  float acc = 0.f;
 #pragma unroll
   for (int t = 0; t < 4; ++t) {  // sub-block 4h+t
-    const int sc = (r.sc >> (8 * t)) & 0xFF, mn = (r.mn >> (8 * t)) & 0xFF;
+    int sc, mn;
+    q4k_scale_min(4 * h + t, r.hdr.y, r.hdr.z, r.hdr.w, sc, mn);
     const uint4 qa = r.q[(t >> 1) * 2], qb = r.q[(t >> 1) * 2 + 1];
     const int shift = (t & 1) * 4;
     const int4 x0 = ldx16(xq + k0 + 32 * t), x1 = ldx16(xq + k0 + 32 * t + 16);
@@ -82,10 +78,104 @@ __device__ __forceinline__ float dot_unit_q4k(const UnitQ4K& r, int u, const int
     dot = dp4a((qb.z >> shift) & 0x0F0F0F0F, x1.z, dot);
     dot = dp4a((qb.w >> shift) & 0x0F0F0F0F, x1.w, dot);
     const int blk = (k0 >> 5) + t;
-    acc = fmaf((float)sc * ldxf(xd + blk), (float)dot, acc);
-    mterm = fmaf((float)mn, ldxf(xs + blk), mterm);
+    acc += d * (float)sc * ldxf(xd + blk) * (float)dot - dmin * (float)mn * ldxf(xs + blk);
   }
-  return d * acc - dmin * mterm;
+  return acc;
+}
+
+// Chunk (coalesced mapping used by the decode GEMV): 64 elements = sub-blocks 2q, 2q+1 of
+// super-block c/4 (q = c % 4), i.e. 32 contiguous quant bytes; lane L owns chunks L + 32 i so a
+// warp's loads cover contiguous 1 KB spans of the quant plane.
+struct ChunkQ4K {
+  uint4 q0, q1;
+  uint4 hdr;
+};
+__device__ __forceinline__ void load_chunk_q4k(const WPlanes& w, int64_t row, int c, ChunkQ4K& r) {
+  const uint8_t* qs = w.p0 + row * w.rb0 + (int64_t)c * 32;
+  r.q0 = ldg_stream(qs);
+  r.q1 = ldg_stream(qs + 16);
+  r.hdr = __ldg(reinterpret_cast<const uint4*>(w.p1 + row * w.rb1 + (int64_t)(c >> 2) * 16));
+}
+__device__ __forceinline__ float dot_chunk_q4k(const ChunkQ4K& r, int c, const int8_t* xq, const float* xd,
+                                               const float* xs) {
+  const float d = __half2float(__ushort_as_half((uint16_t)(r.hdr.x & 0xFFFF)));
+  const float dmin = __half2float(__ushort_as_half((uint16_t)(r.hdr.x >> 16)));
+  const int q = c & 3, sh = 8 * ((2 * q) & 3);  // byte lane of sub-block j0 = 2q inside its word
+  // scales of j0 = 2q and j1 = 2q+1 (both < 4 or both >= 4)
+  const uint32_t lo_sc = r.hdr.y, lo_mn = r.hdr.z, hi = r.hdr.w;
+  int sc0, mn0, sc1, mn1;
+  {
+    const int b0 = (lo_sc >> sh) & 0xFF, b1 = (lo_sc >> (sh + 8)) & 0xFF;
+    const int m0 = (lo_mn >> sh) & 0xFF, m1 = (lo_mn >> (sh + 8)) & 0xFF;
+    const int h0 = (hi >> sh) & 0xFF, h1 = (hi >> (sh + 8)) & 0xFF;
+    if (q < 2) {
+      sc0 = b0 & 63; mn0 = m0 & 63; sc1 = b1 & 63; mn1 = m1 & 63;
+    } else {
+      sc0 = (h0 & 0xF) | ((b0 >> 6) << 4); mn0 = (h0 >> 4) | ((m0 >> 6) << 4);
+      sc1 = (h1 & 0xF) | ((b1 >> 6) << 4); mn1 = (h1 >> 4) | ((m1 >> 6) << 4);
+    }
+  }
+  const int k0 = c * 64;
+  const int4 xa = ldx16(xq + k0), xb = ldx16(xq + k0 + 16), xc = ldx16(xq + k0 + 32), xe = ldx16(xq + k0 + 48);
+  int d0 = 0, d1 = 0;
+  d0 = dp4a(r.q0.x & 0x0F0F0F0F, xa.x, d0); d1 = dp4a((r.q0.x >> 4) & 0x0F0F0F0F, xc.x, d1);
+  d0 = dp4a(r.q0.y & 0x0F0F0F0F, xa.y, d0); d1 = dp4a((r.q0.y >> 4) & 0x0F0F0F0F, xc.y, d1);
+  d0 = dp4a(r.q0.z & 0x0F0F0F0F, xa.z, d0); d1 = dp4a((r.q0.z >> 4) & 0x0F0F0F0F, xc.z, d1);
+  d0 = dp4a(r.q0.w & 0x0F0F0F0F, xa.w, d0); d1 = dp4a((r.q0.w >> 4) & 0x0F0F0F0F, xc.w, d1);
+  d0 = dp4a(r.q1.x & 0x0F0F0F0F, xb.x, d0); d1 = dp4a((r.q1.x >> 4) & 0x0F0F0F0F, xe.x, d1);
+  d0 = dp4a(r.q1.y & 0x0F0F0F0F, xb.y, d0); d1 = dp4a((r.q1.y >> 4) & 0x0F0F0F0F, xe.y, d1);
+  d0 = dp4a(r.q1.z & 0x0F0F0F0F, xb.z, d0); d1 = dp4a((r.q1.z >> 4) & 0x0F0F0F0F, xe.z, d1);
+  d0 = dp4a(r.q1.w & 0x0F0F0F0F, xb.w, d0); d1 = dp4a((r.q1.w >> 4) & 0x0F0F0F0F, xe.w, d1);
+  const int blk = k0 >> 5;
+  const float2 dx = *reinterpret_cast<const float2*>(xd + blk);
+  const float2 sx = *reinterpret_cast<const float2*>(xs + blk);
+  return d * ((float)sc0 * dx.x * (float)d0 + (float)sc1 * dx.y * (float)d1) -
+         dmin * ((float)mn0 * sx.x + (float)mn1 * sx.y);
+}
+
+// ---- Q8_0 chunk: one 32-element block (32 quant bytes + one fp16 scale) -------------------------
+struct ChunkQ8_0 {
+  uint4 q0, q1;
+  float d;
+};
+__device__ __forceinline__ void load_chunk_q8_0(const WPlanes& w, int64_t row, int c, ChunkQ8_0& r) {
+  const uint8_t* qs = w.p0 + row * w.rb0 + (int64_t)c * 32;
+  r.q0 = ldg_stream(qs);
+  r.q1 = ldg_stream(qs + 16);
+  r.d = __half2float(__ldg(reinterpret_cast<const __half*>(w.p1 + row * w.rb1) + c));
+}
+__device__ __forceinline__ float dot_chunk_q8_0(const ChunkQ8_0& r, int c, const int8_t* xq, const float* xd,
+                                                const float* xs) {
+  const int k0 = c * 32;
+  const int4 xa = ldx16(xq + k0), xb = ldx16(xq + k0 + 16);
+  int dot = 0;
+  dot = dp4a(r.q0.x, xa.x, dot); dot = dp4a(r.q0.y, xa.y, dot);
+  dot = dp4a(r.q0.z, xa.z, dot); dot = dp4a(r.q0.w, xa.w, dot);
+  dot = dp4a(r.q1.x, xb.x, dot); dot = dp4a(r.q1.y, xb.y, dot);
+  dot = dp4a(r.q1.z, xb.z, dot); dot = dp4a(r.q1.w, xb.w, dot);
+  (void)xs;
+  return r.d * ldxf(xd + c) * (float)dot;
+}
+
+// ---- Q4_0 chunk: one 32-element block (16 quant bytes + one fp16 scale) -------------------------
+struct ChunkQ4_0 {
+  uint4 q;
+  float d;
+};
+__device__ __forceinline__ void load_chunk_q4_0(const WPlanes& w, int64_t row, int c, ChunkQ4_0& r) {
+  r.q = ldg_stream(w.p0 + row * w.rb0 + (int64_t)c * 16);
+  r.d = __half2float(__ldg(reinterpret_cast<const __half*>(w.p1 + row * w.rb1) + c));
+}
+__device__ __forceinline__ float dot_chunk_q4_0(const ChunkQ4_0& r, int c, const int8_t* xq, const float* xd,
+                                                const float* xs) {
+  const int k0 = c * 32;
+  const int4 xa = ldx16(xq + k0), xb = ldx16(xq + k0 + 16);
+  int dot = 0;
+  dot = dp4a(r.q.x & 0x0F0F0F0F, xa.x, dot); dot = dp4a((r.q.x >> 4) & 0x0F0F0F0F, xb.x, dot);
+  dot = dp4a(r.q.y & 0x0F0F0F0F, xa.y, dot); dot = dp4a((r.q.y >> 4) & 0x0F0F0F0F, xb.y, dot);
+  dot = dp4a(r.q.z & 0x0F0F0F0F, xa.z, dot); dot = dp4a((r.q.z >> 4) & 0x0F0F0F0F, xb.z, dot);
+  dot = dp4a(r.q.w & 0x0F0F0F0F, xa.w, dot); dot = dp4a((r.q.w >> 4) & 0x0F0F0F0F, xb.w, dot);
+  return r.d * (ldxf(xd + c) * (float)dot - 8.f * ldxf(xs + c));
 }
 
 // ---- Q4_0 planes: unit = 4 blocks (128 elements) -------------------------------------------

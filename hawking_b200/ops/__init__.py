@@ -150,7 +150,7 @@ def tc_gemm(w: QWeight, x: torch.Tensor, y: torch.Tensor, status: torch.Tensor, 
     if k_splits == 0 or k_splits is None:
         k_splits = kernels().tc_gemm_splits(w.N, M, w.K, bn, 148) if (atomic or y_zeroed) else 1
     launches.add()
-    kernels().tc_gemm(w.fmt, w.planes[0], w.N, w.K, x, y, atomic, y_zeroed, k_splits, bn, status, PDL)
+    kernels().tc_gemm(w.fmt, w.planes, w.N, w.K, x, y, atomic, y_zeroed, k_splits, bn, status, PDL)
 
 
 def swiglu_bf16(gu: torch.Tensor, F: int, h: torch.Tensor, clear: bool = True):

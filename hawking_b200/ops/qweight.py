@@ -19,29 +19,16 @@ from ..formats.ggml import LAYOUTS, GgmlType, row_bytes
 
 # Byte slices of each block for the plane formats: name -> [(start, end), ...] in plane order.
 _PLANES = {
+    GgmlType.Q4_K: [(16, 144), (0, 16)],   # quants plane + 16-byte header plane
     GgmlType.Q4_0: [(2, 18), (0, 2)],
     GgmlType.Q8_0: [(2, 34), (0, 2)],
     GgmlType.Q5_0: [(6, 22), (0, 2), (2, 6)],
     GgmlType.Q6_K: [(0, 128), (128, 192), (192, 208), (208, 210)],
 }
 DENSE = (GgmlType.F32, GgmlType.F16, GgmlType.BF16)
+RAW_QUANTIZERS = (GgmlType.Q4_K,)
 
 
-def q4k_meta(raw: torch.Tensor, N: int, K: int) -> torch.Tensor:
-    """Predecoded Q4_K side plane [N, K/256 * 20]: d, dmin (fp16 bits) and the eight 6-bit scales
-    and mins of each super-block unpacked to bytes (lossless: the same values as the packed
-    12-byte field; parity crates/hawking-core/src/kernels/mod.rs:1849 predecode_q4_k_scale_table)."""
-    nb = K // 256
-    b = raw.reshape(N, nb, 144)
-    s = b[:, :, 4:16].long()
-    sc = torch.empty(N, nb, 8, dtype=torch.long, device=raw.device)
-    mn = torch.empty_like(sc)
-    sc[..., 0:4] = s[..., 0:4] & 63
-    mn[..., 0:4] = s[..., 4:8] & 63
-    sc[..., 4:8] = (s[..., 8:12] & 0xF) | ((s[..., 0:4] >> 6) << 4)
-    mn[..., 4:8] = (s[..., 8:12] >> 4) | ((s[..., 4:8] >> 6) << 4)
-    out = torch.cat([b[:, :, 0:4], sc.to(torch.uint8), mn.to(torch.uint8)], dim=2)
-    return out.reshape(N, nb * 20).contiguous()
 GEMV_FORMATS = (GgmlType.Q4_K, GgmlType.Q6_K, GgmlType.Q4_0, GgmlType.Q5_0, GgmlType.Q8_0)
 
 
@@ -77,9 +64,6 @@ class QWeight:
             lay = LAYOUTS[fmt]
             blocks = raw.reshape(N, K // lay.block_elems, lay.block_bytes)
             planes = [blocks[:, :, a:b].reshape(N, -1).contiguous() for a, b in _PLANES[fmt]]
-        elif fmt == GgmlType.Q4_K:
-            raw = raw.contiguous()
-            planes = [raw, q4k_meta(raw, N, K)]
         else:
             planes = [raw.contiguous()]
         return QWeight(fmt, N, K, planes)
@@ -102,9 +86,6 @@ class QWeight:
         if fmt in _PLANES:
             nb = K // lay.block_elems
             planes = [torch.empty(N, nb * (b - a), dtype=torch.uint8, device=device) for a, b in _PLANES[fmt]]
-        elif fmt == GgmlType.Q4_K:
-            planes = [torch.empty(N, row_bytes(fmt, K), dtype=torch.uint8, device=device),
-                      torch.empty(N, K // 256 * 20, dtype=torch.uint8, device=device)]
         else:
             planes = [torch.empty(N, row_bytes(fmt, K), dtype=torch.uint8, device=device)]
         return QWeight(fmt, N, K, planes)
@@ -120,9 +101,11 @@ class QWeight:
             dt = {GgmlType.F32: torch.float32, GgmlType.F16: torch.float16, GgmlType.BF16: torch.bfloat16}[fmt]
             w.planes[0].view(dt).copy_(x)
             return w
+        if fmt in RAW_QUANTIZERS:  # the device quantiser writes whole GGUF blocks
+            raw = torch.empty(N, row_bytes(fmt, K), dtype=torch.uint8, device=x.device)
+            kernels().quantize(fmt, x.contiguous().float(), [raw])
+            return QWeight.from_raw(raw, fmt, N, K)
         kernels().quantize(fmt, x.contiguous().float(), w.planes)
-        if fmt == GgmlType.Q4_K:
-            w.planes[1].copy_(q4k_meta(w.planes[0], N, K))
         return w
 
     @staticmethod
