@@ -306,3 +306,145 @@ void attention_decode_launch(const AttnDecodeArgs& a, cudaStream_t s, bool pdl) 
 }
 
 }  // namespace hk
+
+// =================================================================================================
+// Allocation-free entry point: hk_attention_decode_noalloc
+//
+// No counterpart in the reference (its Metal engine has no C entry points of this kind).
+//
+// Some callers of this library cannot call cudaMalloc: an engine embedded in a host process whose
+// own allocator has already reserved the device memory, or a latency-critical decode loop where
+// cudaMalloc/cudaFree (which may synchronise the device) are not allowed. This entry point runs
+// the same split-KV paged decode attention as attention_decode_launch, but its scratch (the
+// per-split partial outputs, their log-sum-exps and the split counters) lives in fixed-size
+// file-scope device arrays instead of caller-provided or freshly allocated buffers. The caller
+// still passes every input and output.
+//
+// Limits: at most kNoAllocPartElems partial-output floats (rows * n_heads * num_splits * head_dim),
+// kNoAllocLseElems log-sum-exps (rows * n_heads * num_splits) and kNoAllocCounters counters
+// (rows * n_kv_heads); larger requests are rejected with HK_NOALLOC_TOO_LARGE. Every GPU that
+// loads this library holds these arrays (about 4.1 MiB) until the process exits.
+//
+// The first call on a device resolves the arrays' device addresses (cudaGetSymbolAddress, with
+// that device current); make that first call before any stream capture. Every call shares the
+// same arrays: calls that overlap on the GPU (different streams, or different host threads with
+// no ordering between their streams) race on the scratch and must not be issued concurrently.
+// The split counters are cleared at the start of every call; the partials are fully overwritten.
+// =================================================================================================
+#include <mutex>
+
+namespace {
+constexpr int64_t kNoAllocPartElems = int64_t(1) << 20;  // 4 MiB of fp32 partial outputs
+constexpr int64_t kNoAllocLseElems = int64_t(1) << 14;   // 64 KiB of fp32 log-sum-exps
+constexpr int64_t kNoAllocCounters = 4096;                // 16 KiB of split counters
+
+static __device__ __align__(256) float g_noalloc_part_o[kNoAllocPartElems];
+static __device__ __align__(256) float g_noalloc_lse[kNoAllocLseElems];
+static __device__ __align__(256) int g_noalloc_counters[kNoAllocCounters];
+
+struct NoAllocScratch {
+  float* part_o = nullptr;
+  float* lse = nullptr;
+  int* counters = nullptr;
+  bool ready = false;
+};
+constexpr int kMaxDevices = 64;
+NoAllocScratch g_noalloc[kMaxDevices];
+std::mutex g_noalloc_mu;
+thread_local std::string g_noalloc_error;
+
+int noalloc_fail(int code, const std::string& msg) {
+  g_noalloc_error = msg;
+  return code;
+}
+}  // namespace
+
+enum HkNoAllocStatus : int {
+  HK_NOALLOC_OK = 0,
+  HK_NOALLOC_BAD_ARG = 1,
+  HK_NOALLOC_TOO_LARGE = 2,
+  HK_NOALLOC_CUDA_ERROR = 3,
+};
+
+// Message of the last failing call on this host thread ("" after a success).
+extern "C" __attribute__((visibility("default"))) const char* hk_attention_decode_noalloc_error() {
+  return g_noalloc_error.c_str();
+}
+
+// Paged GQA decode attention without any allocation (see the block comment above).
+//   q            [rows, n_heads, head_dim] fp32 (already RoPE'd)
+//   k_cache      [num_blocks, n_kv_heads, block_size, head_dim] bf16 (v_cache alike)
+//   block_tables [*, max_blocks] int32; row_seq / row_ctx [rows] int32
+//   out          [rows, n_heads * head_dim] fp32
+//   stream       cudaStream_t to launch on (nullptr = legacy default stream)
+// Returns HK_NOALLOC_OK or an error code; hk_attention_decode_noalloc_error() explains it.
+extern "C" __attribute__((visibility("default"))) int hk_attention_decode_noalloc(
+    const float* q, const void* k_cache, const void* v_cache, const int* block_tables, int max_blocks,
+    const int* row_seq, const int* row_ctx, float scale, int rows, int n_heads, int n_kv_heads, int head_dim,
+    int block_size, int num_splits, float* out, void* stream) {
+  using namespace hk;
+  g_noalloc_error.clear();
+  if (!q || !k_cache || !v_cache || !block_tables || !row_seq || !row_ctx || !out)
+    return noalloc_fail(HK_NOALLOC_BAD_ARG, "null pointer argument");
+  if (rows <= 0 || n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads || num_splits <= 0 || num_splits > 64 ||
+      block_size <= 0 || max_blocks <= 0)
+    return noalloc_fail(HK_NOALLOC_BAD_ARG, "invalid geometry");
+  if (head_dim != 64 && head_dim != 128 && head_dim != 256)
+    return noalloc_fail(HK_NOALLOC_BAD_ARG, "head_dim must be 64, 128 or 256");
+  const int64_t part = (int64_t)rows * n_heads * num_splits * head_dim;
+  const int64_t lse = (int64_t)rows * n_heads * num_splits;
+  const int64_t cnt = (int64_t)rows * n_kv_heads;
+  if (part > kNoAllocPartElems || lse > kNoAllocLseElems || cnt > kNoAllocCounters)
+    return noalloc_fail(HK_NOALLOC_TOO_LARGE,
+                        "request needs " + std::to_string(part) + " partial floats, " + std::to_string(lse) +
+                            " log-sum-exps and " + std::to_string(cnt) + " counters; the fixed scratch holds " +
+                            std::to_string(kNoAllocPartElems) + ", " + std::to_string(kNoAllocLseElems) + " and " +
+                            std::to_string(kNoAllocCounters));
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return noalloc_fail(HK_NOALLOC_CUDA_ERROR, "no current CUDA device");
+  NoAllocScratch sc;
+  {
+    std::lock_guard<std::mutex> g(g_noalloc_mu);
+    NoAllocScratch& s = g_noalloc[dev];
+    if (!s.ready) {  // once per device, with that device current
+      cudaError_t e1 = cudaGetSymbolAddress(reinterpret_cast<void**>(&s.part_o), g_noalloc_part_o);
+      cudaError_t e2 = cudaGetSymbolAddress(reinterpret_cast<void**>(&s.lse), g_noalloc_lse);
+      cudaError_t e3 = cudaGetSymbolAddress(reinterpret_cast<void**>(&s.counters), g_noalloc_counters);
+      if (e1 != cudaSuccess || e2 != cudaSuccess || e3 != cudaSuccess)
+        return noalloc_fail(HK_NOALLOC_CUDA_ERROR, std::string("cudaGetSymbolAddress failed: ") +
+                                                       cudaGetErrorString(e1 != cudaSuccess ? e1 : (e2 != cudaSuccess ? e2 : e3)));
+      s.ready = true;
+    }
+    sc = s;
+  }
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  // The split counters must start at zero (a previous call may have been interrupted).
+  cudaError_t e = cudaMemsetAsync(sc.counters, 0, sizeof(int) * cnt, st);
+  if (e != cudaSuccess) return noalloc_fail(HK_NOALLOC_CUDA_ERROR, std::string("clearing counters: ") + cudaGetErrorString(e));
+  AttnDecodeArgs a{};
+  a.q = q;
+  a.k_cache = reinterpret_cast<const __nv_bfloat16*>(k_cache);
+  a.v_cache = reinterpret_cast<const __nv_bfloat16*>(v_cache);
+  a.block_tables = block_tables;
+  a.max_blocks = max_blocks;
+  a.row_seq = row_seq;
+  a.row_ctx = row_ctx;
+  a.scale = scale;
+  a.R = rows;
+  a.nh = n_heads;
+  a.nkv = n_kv_heads;
+  a.hd = head_dim;
+  a.block_size = block_size;
+  a.num_splits = num_splits;
+  a.part_o = sc.part_o;
+  a.part_lse = sc.lse;
+  a.counters = sc.counters;
+  a.out = out;
+  try {
+    attention_decode_launch(a, st, false);
+  } catch (const std::exception& ex) {
+    return noalloc_fail(HK_NOALLOC_CUDA_ERROR, ex.what());
+  }
+  return HK_NOALLOC_OK;
+}
