@@ -8,13 +8,17 @@
 //    the programmatic-dependent-launch wait, overlapping the previous kernel's tail;
 //  * the input can be the fp32 residual stream: the CTA then computes RMSNorm and the q8 blocks
 //    itself into shared memory (XIN_NORM), removing the separate normalisation kernel;
-//  * the SwiGLU variant runs 32 warps per CTA so its 32 rows form one q8 block of the output.
+//  * the SwiGLU variant runs clusters of 4 CTAs whose 32 rows form one q8 block of the output.
 // Epilogues: STORE (y), RESID (y += acc, fp32 residual stream), SWIGLU_Q8 (h = silu(g) * u -> q8).
 //
 // Parity: replaces the reference's Q4_K/Q6_K/Q8_0 GEMV family (crates/hawking-core/shaders/quant.metal,
 // gemm_q4_k_m_fused*, _pair* gate+up with SwiGLU, _add residual-fused variants, add_rmsnorm_fused_q8
 // feeding them); numerics oracle crates/hawking-core/src/quant.rs:722 (gemv_q4_k_q8k).
 #include "gemv.cuh"
+
+#include <cooperative_groups.h>
+
+namespace cg = cooperative_groups;
 
 namespace hk {
 
@@ -24,31 +28,31 @@ namespace hk {
 template <int FMT> struct Fmt;
 template <> struct Fmt<WF_Q4_K> {
   using T = ChunkQ4K;
-  static constexpr int ELEMS = 64, UPL = 2;
+  static constexpr int ELEMS = 64, UPL = 2, GPC = 4;
   static __device__ __forceinline__ void load(const WPlanes& w, int64_t r, int c, T& u) { load_chunk_q4k(w, r, c, u); }
   static __device__ __forceinline__ float dot(const T& u, int c, const int8_t* q, const float* d, const float* s) {
-    return dot_chunk_q4k(u, c, q, d, s);
+    return dot_chunk_q4k<GPC>(u, c, q, d, s);
   }
 };
 template <> struct Fmt<WF_Q8_0> {
   using T = ChunkQ8_0;
-  static constexpr int ELEMS = 32, UPL = 4;
+  static constexpr int ELEMS = 32, UPL = 4, GPC = 2;
   static __device__ __forceinline__ void load(const WPlanes& w, int64_t r, int c, T& u) { load_chunk_q8_0(w, r, c, u); }
   static __device__ __forceinline__ float dot(const T& u, int c, const int8_t* q, const float* d, const float* s) {
-    return dot_chunk_q8_0(u, c, q, d, s);
+    return dot_chunk_q8_0<GPC>(u, c, q, d, s);
   }
 };
 template <> struct Fmt<WF_Q4_0> {
   using T = ChunkQ4_0;
-  static constexpr int ELEMS = 32, UPL = 4;
+  static constexpr int ELEMS = 32, UPL = 4, GPC = 2;
   static __device__ __forceinline__ void load(const WPlanes& w, int64_t r, int c, T& u) { load_chunk_q4_0(w, r, c, u); }
   static __device__ __forceinline__ float dot(const T& u, int c, const int8_t* q, const float* d, const float* s) {
-    return dot_chunk_q4_0(u, c, q, d, s);
+    return dot_chunk_q4_0<GPC>(u, c, q, d, s);
   }
 };
 template <> struct Fmt<WF_Q6_K> {
   using T = UnitQ6K;
-  static constexpr int ELEMS = 128, UPL = 1;
+  static constexpr int ELEMS = 128, UPL = 1, GPC = 0;
   static __device__ __forceinline__ void load(const WPlanes& w, int64_t r, int c, T& u) { load_unit_q6k(w, r, c, u); }
   static __device__ __forceinline__ float dot(const T& u, int c, const int8_t* q, const float* d, const float* s) {
     return dot_unit_q6k(u, c, q, d, s);
@@ -56,7 +60,7 @@ template <> struct Fmt<WF_Q6_K> {
 };
 template <> struct Fmt<WF_Q5_0> {
   using T = UnitQ5_0;
-  static constexpr int ELEMS = 128, UPL = 1;
+  static constexpr int ELEMS = 128, UPL = 1, GPC = 0;
   static __device__ __forceinline__ void load(const WPlanes& w, int64_t r, int c, T& u) { load_unit_q5_0(w, r, c, u); }
   static __device__ __forceinline__ float dot(const T& u, int c, const int8_t* q, const float* d, const float* s) {
     return dot_unit_q5_0(u, c, q, d, s);
@@ -117,7 +121,7 @@ __device__ __forceinline__ void row_dot(const WPlanes& w, int64_t row, int n_uni
 // CTA-cooperative RMSNorm + q8 of nb fp32 rows into shared memory. Thread t handles elements
 // t + e * blockDim.x (EPT of them, all loaded before any reduction), so each warp owns whole
 // 32-element blocks. Columns are processed one after another.
-template <int EPT>
+template <int EPT, int GPC>
 __device__ __forceinline__ void norm_q8_to_smem(const GemvArgs& a, int nb, int8_t* sq, float* sd, float* ss,
                                                 float* red) {
   const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31;
@@ -156,7 +160,7 @@ __device__ __forceinline__ void norm_q8_to_smem(const GemvArgs& a, int nb, int8_
         const float d = amax / 127.f;
         const int q = amax > 0.f ? __float2int_rn(x / d) : 0;
         const float qs = warp_sum((float)q);
-        sq[b * K + i] = (int8_t)q;
+        sq[b * K + 16 * swz_granule<GPC>(i >> 4) + (i & 15)] = (int8_t)q;
         if (lane == 0) {
           sd[b * (K / 32) + (i >> 5)] = d;
           ss[b * (K / 32) + (i >> 5)] = d * qs;
@@ -167,14 +171,16 @@ __device__ __forceinline__ void norm_q8_to_smem(const GemvArgs& a, int nb, int8_
   __syncthreads();
 }
 
-// Kernel: one warp per row (STORE / RESID), or one gate/up row pair per warp (SWIGLU_Q8, 32
-// warps so the CTA's 32 rows form one q8 block of the output).
+// Kernel: one warp per row (STORE / RESID) or per gate/up row pair (SWIGLU_Q8), 8 warps per CTA.
+// SWIGLU_Q8 launches clusters of 4 CTAs: their 4 x 8 rows form one 32-element q8 block of the
+// output, which the cluster's first CTA quantises after reading the other CTAs' values through
+// distributed shared memory.
 template <int FMT, int NB, int EPI, int XIN>
-__global__ void __launch_bounds__(EPI == EPI_SWIGLU_Q8 ? 1024 : 256) gemv_kernel(GemvArgs a, int nb) {
+__global__ void __launch_bounds__(256, (NB == 1 && XIN == XIN_Q8) ? (EPI == EPI_SWIGLU_Q8 ? 3 : 4) : 1) gemv_kernel(GemvArgs a, int nb) {
   extern __shared__ __align__(16) uint8_t gsm[];
   __shared__ float red[8 * 32];
-  __shared__ float hbuf[NB][32];
-  constexpr int WARPS = EPI == EPI_SWIGLU_Q8 ? 32 : 8;
+  __shared__ float hbuf[NB][8];
+  constexpr int WARPS = 8;
   constexpr int UPL = Fmt<FMT>::UPL;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_units = a.K / Fmt<FMT>::ELEMS;
@@ -190,7 +196,7 @@ __global__ void __launch_bounds__(EPI == EPI_SWIGLU_Q8 ? 1024 : 256) gemv_kernel
   }
   pdl_wait();
 
-  // 2) activations into shared memory
+  // 2) activations into shared memory (granule-swizzled, see swz_granule)
   XSrc x;
   {
     int8_t* sq = reinterpret_cast<int8_t*>(gsm);
@@ -199,13 +205,14 @@ __global__ void __launch_bounds__(EPI == EPI_SWIGLU_Q8 ? 1024 : 256) gemv_kernel
     if constexpr (XIN == XIN_NORM) {
       constexpr int NT = WARPS * 32;
       constexpr int EPT = (4096 + NT - 1) / NT;
-      norm_q8_to_smem<EPT>(a, nb, sq, sd, ss, red);
+      norm_q8_to_smem<EPT, Fmt<FMT>::GPC>(a, nb, sq, sd, ss, red);
     } else {
       const int nt = blockDim.x, tid = threadIdx.x;
       const int kq16 = a.K / 16, ks = a.K / 32;
       for (int i = tid; i < nb * kq16; i += nt) {
         const int b = i / kq16, c = i - b * kq16;
-        reinterpret_cast<int4*>(sq)[i] = __ldg(reinterpret_cast<const int4*>(a.xq + (int64_t)b * a.x_stride_q) + c);
+        reinterpret_cast<int4*>(sq)[b * kq16 + swz_granule<Fmt<FMT>::GPC>(c)] =
+            __ldg(reinterpret_cast<const int4*>(a.xq + (int64_t)b * a.x_stride_q) + c);
       }
       for (int i = tid; i < nb * ks; i += nt) {
         const int b = i / ks, c = i - b * ks;
@@ -233,22 +240,26 @@ __global__ void __launch_bounds__(EPI == EPI_SWIGLU_Q8 ? 1024 : 256) gemv_kernel
 #pragma unroll
       for (int b = 0; b < NB; ++b) hbuf[b][warp] = live ? g[b] / (1.f + __expf(-g[b])) * u[b] : 0.f;
     }
-    __syncthreads();
     pdl_launch();
-    if (warp < nb) {
-      const int b = warp;
-      const int64_t n = (int64_t)blockIdx.x * 32 + lane;
-      const float v = hbuf[b][lane];
-      const float amax = warp_max(fabsf(v));
-      const float d = amax / 127.f;
-      const int q = amax > 0.f ? __float2int_rn(v / d) : 0;
-      const float qs = warp_sum((float)q);
-      if (n < a.N) a.oq[b * a.o_stride_q + n] = (int8_t)q;
-      if (lane == 0 && n < a.N) {
-        a.od[b * a.o_stride_s + (n >> 5)] = d;
-        a.os[b * a.o_stride_s + (n >> 5)] = d * qs;
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();  // every CTA's hbuf is written and visible to the cluster
+    if (cluster.block_rank() == 0) {
+      const int64_t n = (int64_t)(blockIdx.x / 4) * 32 + lane;  // this cluster's q8 block
+      const float* src = cluster.map_shared_rank(&hbuf[0][0], lane >> 3);
+      for (int b = warp; b < nb; b += WARPS) {
+        const float v = src[b * 8 + (lane & 7)];
+        const float amax = warp_max(fabsf(v));
+        const float d = amax / 127.f;
+        const int q = amax > 0.f ? __float2int_rn(v / d) : 0;
+        const float qs = warp_sum((float)q);
+        if (n < a.N) a.oq[b * a.o_stride_q + n] = (int8_t)q;
+        if (lane == 0 && n < a.N) {
+          a.od[b * a.o_stride_s + (n >> 5)] = d;
+          a.os[b * a.o_stride_s + (n >> 5)] = d * qs;
+        }
       }
     }
+    cluster.sync();  // the other CTAs' shared memory stays alive until the first CTA has read it
   } else {
     if (!live) { pdl_launch(); return; }
     float acc[NB];
@@ -271,13 +282,14 @@ __global__ void __launch_bounds__(EPI == EPI_SWIGLU_Q8 ? 1024 : 256) gemv_kernel
 
 template <int FMT, int EPI, int XIN>
 static void dispatch_nb(const GemvArgs& a, int nb, cudaStream_t s, bool pdl) {
-  const int rows_per_cta = (EPI == EPI_SWIGLU_Q8) ? 32 : 8;
-  const int threads = (EPI == EPI_SWIGLU_Q8) ? 1024 : 256;
+  const int rows_per_cta = 8;
+  const int threads = 256;
   dim3 grid((a.N + rows_per_cta - 1) / rows_per_cta), block(threads);
   const size_t smem = (size_t)nb * a.K + 2 * (size_t)nb * (a.K / 32) * 4;  // q8 activations staged in smem
   auto go = [&](auto kern) {
     if (smem > 48 * 1024) HK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    launch(kern, grid, block, smem, s, pdl, a, nb);
+    if (EPI == EPI_SWIGLU_Q8) launch_cluster(kern, grid, block, smem, s, pdl, 4, a, nb);
+    else launch(kern, grid, block, smem, s, pdl, a, nb);
   };
   if (nb == 1) go(gemv_kernel<FMT, 1, EPI, XIN>);
   else if (nb == 2) go(gemv_kernel<FMT, 2, EPI, XIN>);

@@ -24,6 +24,25 @@ namespace hk {
 __device__ __forceinline__ int4 ldx16(const int8_t* p) { return *reinterpret_cast<const int4*>(p); }
 __device__ __forceinline__ float ldxf(const float* p) { return *p; }
 
+// Shared-memory swizzle of the q8 activation bytes, in 16-byte granules. With the chunk mapping,
+// lane L reads granule g of chunk c = L + 32 i, so 8 consecutive lanes (one phase of a 16-byte
+// shared load) read granules 4 (or 2) apart and hit the same banks. Permuting the granules of a
+// chunk by bits of the chunk index spreads those 8 reads over all 32 banks:
+//   GPC = 4 (64-byte chunks, Q4_K): granule g of chunk c is stored at g ^ ((c >> 1) & 3)
+//   GPC = 2 (32-byte chunks, Q8_0 / Q4_0): granule g of chunk c is stored at g ^ ((c >> 2) & 1)
+// The permutation stays inside each aligned group of 4 (or 2) granules, so it is a bijection on
+// any K that is a multiple of 64. GPC = 0 is the identity (global activations, unit formats).
+template <int GPC>
+__device__ __forceinline__ int swz_granule(int G) {
+  if constexpr (GPC == 4) return G ^ ((G >> 3) & 3);
+  else if constexpr (GPC == 2) return G ^ ((G >> 3) & 1);
+  else return G;
+}
+template <int GPC>
+__device__ __forceinline__ int4 ldx_granule(const int8_t* xq, int G) {
+  return ldx16(xq + 16 * swz_granule<GPC>(G));
+}
+
 // Q4_K/Q5_K six-bit scale & min of sub-block j (0..7) from the 12 scale bytes packed in 3 words.
 __device__ __forceinline__ void q4k_scale_min(int j, uint32_t s0, uint32_t s1, uint32_t s2, int& sc, int& mn) {
   auto B = [&](int i) -> int {
@@ -96,6 +115,7 @@ __device__ __forceinline__ void load_chunk_q4k(const WPlanes& w, int64_t row, in
   r.q1 = ldg_stream(qs + 16);
   r.hdr = __ldg(reinterpret_cast<const uint4*>(w.p1 + row * w.rb1 + (int64_t)(c >> 2) * 16));
 }
+template <int GPC = 0>
 __device__ __forceinline__ float dot_chunk_q4k(const ChunkQ4K& r, int c, const int8_t* xq, const float* xd,
                                                const float* xs) {
   const float d = __half2float(__ushort_as_half((uint16_t)(r.hdr.x & 0xFFFF)));
@@ -116,7 +136,8 @@ __device__ __forceinline__ float dot_chunk_q4k(const ChunkQ4K& r, int c, const i
     }
   }
   const int k0 = c * 64;
-  const int4 xa = ldx16(xq + k0), xb = ldx16(xq + k0 + 16), xc = ldx16(xq + k0 + 32), xe = ldx16(xq + k0 + 48);
+  const int4 xa = ldx_granule<GPC>(xq, 4 * c), xb = ldx_granule<GPC>(xq, 4 * c + 1);
+  const int4 xc = ldx_granule<GPC>(xq, 4 * c + 2), xe = ldx_granule<GPC>(xq, 4 * c + 3);
   int d0 = 0, d1 = 0;
   d0 = dp4a(r.q0.x & 0x0F0F0F0F, xa.x, d0); d1 = dp4a((r.q0.x >> 4) & 0x0F0F0F0F, xc.x, d1);
   d0 = dp4a(r.q0.y & 0x0F0F0F0F, xa.y, d0); d1 = dp4a((r.q0.y >> 4) & 0x0F0F0F0F, xc.y, d1);
@@ -144,10 +165,10 @@ __device__ __forceinline__ void load_chunk_q8_0(const WPlanes& w, int64_t row, i
   r.q1 = ldg_stream(qs + 16);
   r.d = __half2float(__ldg(reinterpret_cast<const __half*>(w.p1 + row * w.rb1) + c));
 }
+template <int GPC = 0>
 __device__ __forceinline__ float dot_chunk_q8_0(const ChunkQ8_0& r, int c, const int8_t* xq, const float* xd,
                                                 const float* xs) {
-  const int k0 = c * 32;
-  const int4 xa = ldx16(xq + k0), xb = ldx16(xq + k0 + 16);
+  const int4 xa = ldx_granule<GPC>(xq, 2 * c), xb = ldx_granule<GPC>(xq, 2 * c + 1);
   int dot = 0;
   dot = dp4a(r.q0.x, xa.x, dot); dot = dp4a(r.q0.y, xa.y, dot);
   dot = dp4a(r.q0.z, xa.z, dot); dot = dp4a(r.q0.w, xa.w, dot);
@@ -166,10 +187,10 @@ __device__ __forceinline__ void load_chunk_q4_0(const WPlanes& w, int64_t row, i
   r.q = ldg_stream(w.p0 + row * w.rb0 + (int64_t)c * 16);
   r.d = __half2float(__ldg(reinterpret_cast<const __half*>(w.p1 + row * w.rb1) + c));
 }
+template <int GPC = 0>
 __device__ __forceinline__ float dot_chunk_q4_0(const ChunkQ4_0& r, int c, const int8_t* xq, const float* xd,
                                                 const float* xs) {
-  const int k0 = c * 32;
-  const int4 xa = ldx16(xq + k0), xb = ldx16(xq + k0 + 16);
+  const int4 xa = ldx_granule<GPC>(xq, 2 * c), xb = ldx_granule<GPC>(xq, 2 * c + 1);
   int dot = 0;
   dot = dp4a(r.q.x & 0x0F0F0F0F, xa.x, dot); dot = dp4a((r.q.x >> 4) & 0x0F0F0F0F, xb.x, dot);
   dot = dp4a(r.q.y & 0x0F0F0F0F, xa.y, dot); dot = dp4a((r.q.y >> 4) & 0x0F0F0F0F, xb.y, dot);
