@@ -42,6 +42,9 @@ def parse():
     ap.add_argument("--ttft-runs", type=int, default=3)
     ap.add_argument("--e2e-steps", type=int, default=0, help="0 = same as --steps")
     ap.add_argument("--layers", type=int, default=0, help="override layer count (debug only; invalidates the number)")
+    ap.add_argument("--profile-step", action="store_true",
+                    help="run one eager decode step between cudaProfilerStart/Stop (for ncu --profile-from-start off) "
+                         "and exit without a result line")
     return ap.parse_args()
 
 
@@ -142,6 +145,16 @@ def main():
 
     # ---- bs1 (or --batch) device-timed decode ----
     seqs = setup_decode(B, 1_000_000)
+    if args.profile_step:
+        for _ in range(W):
+            m.forward(B, "greedy")
+        torch.cuda.synchronize()
+        torch.cuda.cudart().cudaProfilerStart()
+        m.forward(B, "greedy")
+        torch.cuda.synchronize()
+        torch.cuda.cudart().cudaProfilerStop()
+        print(json.dumps({"profile_step": True, "launches": m.launches_per_forward}))
+        return 0
     ms1, clocks = timed_decode(B)
     launches = m.launches_per_graph
     for s in seqs:

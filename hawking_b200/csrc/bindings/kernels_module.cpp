@@ -157,14 +157,15 @@ void attention_decode(const Tensor& q, const Tensor& k_cache, const Tensor& v_ca
                       const Tensor& part_o, const Tensor& part_lse, const optional<Tensor>& out,
                       const optional<Tensor>& oq, const optional<Tensor>& od, const optional<Tensor>& os,
                       const optional<Tensor>& sinks, const optional<Tensor>& out_bf16,
-                      const optional<Tensor>& counters, bool pdl) {
+                      const optional<Tensor>& counters, bool pdl, bool cluster) {
   check_cuda(q, "q");
   TORCH_CHECK(q.dim() == 3 && q.scalar_type() == at::kFloat, "q must be fp32 [R, nh, hd]");
   TORCH_CHECK(k_cache.dim() == 4 && k_cache.scalar_type() == at::kBFloat16, "k_cache must be bf16 [blocks, nkv, bs, hd]");
   TORCH_CHECK(block_tables.scalar_type() == at::kInt && row_seq.scalar_type() == at::kInt &&
                   row_ctx.scalar_type() == at::kInt, "block tables / rows must be int32");
   const int R = (int)q.size(0), nh = (int)q.size(1), hd = (int)q.size(2);
-  TORCH_CHECK(part_o.numel() >= (int64_t)R * nh * num_splits * hd && part_lse.numel() >= (int64_t)R * nh * num_splits,
+  TORCH_CHECK(cluster || (part_o.numel() >= (int64_t)R * nh * num_splits * hd &&
+                          part_lse.numel() >= (int64_t)R * nh * num_splits),
               "attention: scratch too small");
   hk::AttnDecodeArgs a{};
   a.q = ptr<float>(q);
@@ -192,7 +193,8 @@ void attention_decode(const Tensor& q, const Tensor& k_cache, const Tensor& v_ca
   a.counters = optr<int>(counters);
   TORCH_CHECK(!counters.has_value() || counters->numel() >= (int64_t)R * a.nkv, "attention: counters too small");
   const c10::cuda::CUDAGuard g(q.device());
-  hk::attention_decode_launch(a, cur_stream(), pdl);
+  if (cluster) hk::attention_decode_cluster_launch(a, cur_stream(), pdl);
+  else hk::attention_decode_launch(a, cur_stream(), pdl);
 }
 
 void argmax(const Tensor& logits, const Tensor& out, bool pdl) {
@@ -261,7 +263,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("block_tables"), py::arg("row_seq"), py::arg("row_ctx"), py::arg("scale"), py::arg("num_splits"),
         py::arg("part_o"), py::arg("part_lse"), py::arg("out") = py::none(), py::arg("oq") = py::none(),
         py::arg("od") = py::none(), py::arg("os") = py::none(), py::arg("sinks") = py::none(),
-        py::arg("out_bf16") = py::none(), py::arg("counters") = py::none(), py::arg("pdl") = false);
+        py::arg("out_bf16") = py::none(), py::arg("counters") = py::none(), py::arg("pdl") = false,
+        py::arg("cluster") = false);
   m.def("argmax", &argmax, py::arg("logits"), py::arg("out"), py::arg("pdl") = false);
   m.def("sample", &sample, py::arg("logits"), py::arg("temperature"), py::arg("top_k"), py::arg("top_p"),
         py::arg("rep_penalty"), py::arg("recent"), py::arg("uniforms"), py::arg("out"), py::arg("pdl") = false);

@@ -15,6 +15,7 @@ using namespace hk;
 
 void bind_engine(py::module_& m);   // engine_bindings.cpp
 void bind_formats(py::module_& m);  // formats_bindings.cpp
+void bind_serve(py::module_& m);    // serve_bindings.cpp
 
 namespace {
 
@@ -248,4 +249,5 @@ PYBIND11_MODULE(_native, m) {
 
   bind_formats(m);
   bind_engine(m);
+  bind_serve(m);
 }

@@ -108,6 +108,9 @@ struct AttnDecodeArgs {
   int* counters;               // [R * nkv] zero-initialised split counters (scratch; reset after use)
 };
 void attention_decode_launch(const AttnDecodeArgs& a, cudaStream_t s, bool pdl);
+// Cluster variant (num_splits in {1, 2, 4, 8}): the splits of one (row, kv head) merge through
+// distributed shared memory; part_o / part_lse / counters are not used.
+void attention_decode_cluster_launch(const AttnDecodeArgs& a, cudaStream_t s, bool pdl);
 
 // Greedy: index of the max logit per row (lowest index on ties).
 void argmax_launch(const float* logits, int64_t stride, int rows, int V, int* out, cudaStream_t s, bool pdl);

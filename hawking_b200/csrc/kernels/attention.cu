@@ -17,6 +17,10 @@
 // CPU oracle crates/hawking-core/src/attn.rs:23 (mha_decode_step).
 #include "decode_ops.cuh"
 
+#include <cooperative_groups.h>
+
+namespace cg = cooperative_groups;
+
 namespace hk {
 
 template <int HPL>
@@ -270,6 +274,236 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnDecodeArgs a) {
         a.os[(int64_t)r * (width / 32) + (col0 >> 5) + blk] = dq * qsum;
       }
     }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Cluster variant: the S = num_splits CTAs of one (row, kv head) form a thread-block cluster. CTA
+// s owns the s-th contiguous token range and its WARPS warps interleave over tiles of T tokens as
+// above. The warps' partials are folded into one (max, sum, o) per CTA in shared memory; after a
+// cluster barrier each CTA merges whole 32-dim output blocks across the S CTAs by reading their
+// shared memory directly (distributed shared memory) and writes them. No global scratch, no split
+// counters, no second pass over memory.
+template <int G, int HPL, int WARPS>
+__global__ void __launch_bounds__(WARPS * 32) attn_decode_cluster_kernel(AttnDecodeArgs a) {
+  constexpr int T = (32 / G) > (HPL >= 8 ? 4 : 8) ? (HPL >= 8 ? 4 : 8) : (32 / G);
+  constexpr int NV = G * T;
+  constexpr int HD = HPL * 32;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int S = (int)cluster.num_blocks();
+  const int split = (int)cluster.block_rank();
+  const int kvh = blockIdx.y, r = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __shared__ float s_wm[WARPS][G];
+  __shared__ float s_m[G], s_l[G];
+  __shared__ __align__(16) float s_o[G][HD];
+  for (int i = threadIdx.x; i < G * HD; i += blockDim.x) (&s_o[0][0])[i] = 0.f;
+  if (threadIdx.x < G) s_l[threadIdx.x] = 0.f;
+
+  pdl_wait();
+  const int ctx = a.row_ctx[r];
+  const int* btab = a.block_tables + (int64_t)a.row_seq[r] * a.max_blocks;
+  const int chunk = ((ctx + S - 1) / S + T - 1) / T * T;
+  const int t0 = split * chunk, t1 = min(ctx, t0 + chunk);
+
+  float q[G][HPL];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const float* qp = a.q + ((int64_t)r * a.nh + kvh * G + g) * HD + lane * HPL;
+#pragma unroll
+    for (int i = 0; i < HPL; ++i) q[g][i] = qp[i] * a.scale;
+  }
+  float m[G], l[G], acc[G][HPL];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    m[g] = -INFINITY;
+    l[g] = 0.f;
+#pragma unroll
+    for (int i = 0; i < HPL; ++i) acc[g][i] = 0.f;
+  }
+  const int bs = a.block_size;
+  const int64_t head_stride = (int64_t)bs * HD;
+  for (int tt = t0 + warp * T; tt < t1; tt += WARPS * T) {
+    const int blk_a = btab[tt / bs];
+    const int blk_b = btab[min(tt + T - 1, t1 - 1) / bs];
+    float kreg[T][HPL], vreg[T][HPL];
+#pragma unroll
+    for (int j = 0; j < T; ++j) {
+      const int t = tt + j;
+      if (t < t1) {
+        const int blk = (t / bs == tt / bs) ? blk_a : blk_b;
+        const int64_t off = ((int64_t)blk * a.nkv + kvh) * head_stride + (int64_t)(t % bs) * HD + lane * HPL;
+        load_bf16<HPL>(a.k_cache + off, kreg[j]);
+        load_bf16<HPL>(a.v_cache + off, vreg[j]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < HPL; ++i) { kreg[j][i] = 0.f; vreg[j][i] = 0.f; }
+      }
+    }
+    float part[32];
+#pragma unroll
+    for (int v = NV; v < 32; ++v) part[v] = 0.f;
+#pragma unroll
+    for (int j = 0; j < T; ++j) {
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float sdot = 0.f;
+#pragma unroll
+        for (int i = 0; i < HPL; ++i) sdot = fmaf(q[g][i], kreg[j][i], sdot);
+        part[g * T + j] = sdot;
+      }
+    }
+#pragma unroll
+    for (int o = 16, n = 32; o > 0; o >>= 1, n >>= 1) {
+      const bool up = lane & o;
+#pragma unroll
+      for (int i = 0; i < n / 2; ++i) {
+        const float send = up ? part[i] : part[i + n / 2];
+        const float keep = up ? part[i + n / 2] : part[i];
+        part[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+      }
+    }
+    const int my_g = min(lane / T, G - 1), my_j = lane % T;
+    const float score = (lane < NV && tt + my_j < t1) ? part[0] : -INFINITY;
+    float tmax = score;
+#pragma unroll
+    for (int o = T / 2; o > 0; o >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
+    float p_new_m[G], alpha[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float tm = __shfl_sync(0xffffffffu, tmax, g * T);
+      p_new_m[g] = fmaxf(m[g], tm);
+      alpha[g] = __expf(m[g] - p_new_m[g]);
+    }
+    float mg = p_new_m[0];
+#pragma unroll
+    for (int g = 1; g < G; ++g)
+      if (my_g == g) mg = p_new_m[g];
+    const float p = (score == -INFINITY) ? 0.f : __expf(score - mg);
+    float psum = p;
+#pragma unroll
+    for (int o = T / 2; o > 0; o >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, o);
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float ps = __shfl_sync(0xffffffffu, psum, g * T);
+      l[g] = l[g] * alpha[g] + ps;
+      m[g] = p_new_m[g];
+#pragma unroll
+      for (int i = 0; i < HPL; ++i) acc[g][i] *= alpha[g];
+    }
+#pragma unroll
+    for (int j = 0; j < T; ++j) {
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float pg = __shfl_sync(0xffffffffu, p, g * T + j);
+#pragma unroll
+        for (int i = 0; i < HPL; ++i) acc[g][i] = fmaf(pg, vreg[j][i], acc[g][i]);
+      }
+    }
+  }
+  // ---- fold the warps into one (m, l, o) per CTA ----
+  if (lane == 0) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) s_wm[warp][g] = m[g];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < WARPS; ++w) M = fmaxf(M, s_wm[w][g]);
+    const float f = (m[g] == -INFINITY) ? 0.f : __expf(m[g] - M);
+    if (f != 0.f) {
+#pragma unroll
+      for (int i = 0; i < HPL; ++i) atomicAdd(&s_o[g][lane * HPL + i], acc[g][i] * f);
+      if (lane == 0) atomicAdd(&s_l[g], l[g] * f);
+    }
+    if (warp == 0 && lane == 0) s_m[g] = M;
+  }
+  pdl_launch();
+  cluster.sync();  // every CTA's (m, l, o) is complete and visible to the cluster
+
+  // ---- merge whole 32-dim blocks across the cluster; CTA s takes blocks s, s + S, ... ----
+  const int64_t width = (int64_t)a.nh * HD;
+  const int64_t col0 = (int64_t)kvh * G * HD;
+  constexpr int NBLK = G * HD / 32;
+  for (int blk = split + S * warp; blk < NBLK; blk += S * WARPS) {
+    const int idx = blk * 32 + lane;
+    const int g = idx / HD, d = idx % HD;
+    float mk[8], lk[8], ok[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if (k < S) {
+        mk[k] = *cluster.map_shared_rank(&s_m[g], k);
+        lk[k] = *cluster.map_shared_rank(&s_l[g], k);
+        ok[k] = *cluster.map_shared_rank(&s_o[g][d], k);
+      }
+    }
+    float M = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (k < S) M = fmaxf(M, mk[k]);
+    const float sink = a.sinks ? a.sinks[kvh * G + g] : -INFINITY;
+    M = fmaxf(M, sink);
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if (k < S && mk[k] != -INFINITY) {
+        const float f = __expf(mk[k] - M);
+        L += lk[k] * f;
+        O += ok[k] * f;
+      }
+    }
+    if (a.sinks) L += __expf(sink - M);
+    const float v = L > 0.f ? O / L : 0.f;
+    if (a.out) a.out[(int64_t)r * width + col0 + idx] = v;
+    if (a.out_bf16) a.out_bf16[(int64_t)r * width + col0 + idx] = __float2bfloat16(v);
+    if (a.oq) {
+      const float amax = warp_max(fabsf(v));
+      const float dq = amax / 127.f;
+      const int qv = amax > 0.f ? __float2int_rn(v / dq) : 0;
+      const float qsum = warp_sum((float)qv);
+      a.oq[(int64_t)r * width + col0 + idx] = (int8_t)qv;
+      if (lane == 0) {
+        a.od[(int64_t)r * (width / 32) + (col0 >> 5) + blk] = dq;
+        a.os[(int64_t)r * (width / 32) + (col0 >> 5) + blk] = dq * qsum;
+      }
+    }
+  }
+  cluster.sync();  // keep this CTA's shared memory alive until every CTA has read it
+}
+
+template <int G, int HPL>
+static void launch_cluster_g(const AttnDecodeArgs& a, cudaStream_t s, bool pdl) {
+  constexpr int WARPS = G * HPL <= 16 ? 16 : 8;
+  launch_cluster(attn_decode_cluster_kernel<G, HPL, WARPS>, dim3(a.num_splits, a.nkv, a.R), dim3(WARPS * 32), 0,
+                 s, pdl, a.num_splits, a);
+}
+
+template <int HPL>
+static void launch_cluster_hpl(const AttnDecodeArgs& a, int G, cudaStream_t s, bool pdl) {
+  switch (G) {
+    case 1: launch_cluster_g<1, HPL>(a, s, pdl); break;
+    case 2: launch_cluster_g<2, HPL>(a, s, pdl); break;
+    case 4: launch_cluster_g<4, HPL>(a, s, pdl); break;
+    case 8: launch_cluster_g<8, HPL>(a, s, pdl); break;
+    case 16:
+      if constexpr (HPL <= 4) { launch_cluster_g<16, HPL>(a, s, pdl); break; }
+      [[fallthrough]];
+    default: throw std::runtime_error("attention: GQA group must be 1, 2, 4, 8 or 16");
+  }
+}
+
+void attention_decode_cluster_launch(const AttnDecodeArgs& a, cudaStream_t s, bool pdl) {
+  if (a.nh % a.nkv) throw std::runtime_error("attention: n_heads must be a multiple of n_kv_heads");
+  if (a.num_splits != 1 && a.num_splits != 2 && a.num_splits != 4 && a.num_splits != 8)
+    throw std::runtime_error("attention (cluster): num_splits must be 1, 2, 4 or 8");
+  const int G = a.nh / a.nkv;
+  switch (a.hd) {
+    case 64: launch_cluster_hpl<2>(a, G, s, pdl); break;
+    case 128: launch_cluster_hpl<4>(a, G, s, pdl); break;
+    case 256: launch_cluster_hpl<8>(a, G, s, pdl); break;
+    default: throw std::runtime_error("attention: head_dim must be 64, 128 or 256");
   }
 }
 

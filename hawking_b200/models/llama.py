@@ -231,8 +231,12 @@ class LlamaModel:
         self.launches_per_forward = 0
 
     def num_splits(self, rows: int) -> int:
-        target = 2 * 148
-        return max(1, min(self.max_splits, -(-target // (rows * self.cfg.n_kv_heads))))
+        """KV splits per (row, kv head): the smallest power of two (at most 8, the portable
+        thread-block cluster size) that puts at least one CTA on every SM."""
+        s = 1
+        while s < min(8, self.max_splits) and rows * self.cfg.n_kv_heads * s < 148:
+            s *= 2
+        return s
 
     # ---- forward ----
     def _gemv_cols(self, fn, rows):

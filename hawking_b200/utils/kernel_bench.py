@@ -79,7 +79,7 @@ def build_cases(dev: str = "cuda", ctx: int = 2048, rows: int = 1, only=None):
                                wgu[0][0].nbytes + wgu[0][1].nbytes)
     cases["down"] = (lambda i: ops.gemv(wd[i % len(wd)][0], ha, y[:, :H], residual=True), wd[0][0].nbytes)
 
-    if only is not None and "attention" not in only and "lm_head" not in only:
+    if only is not None and not any(c.startswith("attention") or c == "lm_head" for c in only):
         return cases
     nblk = (ctx + BS - 1) // BS
     kc = torch.randn(nblk * rows, NKV, BS, HD, device=dev).bfloat16()
@@ -88,14 +88,21 @@ def build_cases(dev: str = "cuda", ctx: int = 2048, rows: int = 1, only=None):
     rs = torch.arange(rows, dtype=torch.int32, device=dev)
     rc = torch.full((rows,), ctx, dtype=torch.int32, device=dev)
     q = torch.randn(rows, NH, HD, device=dev)
-    splits = max(1, min(64, (296 + rows * NKV - 1) // (rows * NKV)))
-    po = torch.zeros(rows * splits * NH * HD, device=dev)
-    pl = torch.zeros(rows * splits * NH, device=dev)
+    splits = 1
+    while splits < 8 and rows * NKV * splits < 148:
+        splits *= 2
+    old_splits = max(1, min(64, (296 + rows * NKV - 1) // (rows * NKV)))
+    po = torch.zeros(rows * old_splits * NH * HD, device=dev)
+    pl = torch.zeros(rows * old_splits * NH, device=dev)
     cnt = torch.zeros(rows * NKV, dtype=torch.int32, device=dev)
     att = Q8Act(rows, NH * HD, dev)
     cases["attention"] = (
         lambda i: ops.attention_decode(q, kc, vc, tables, rs, rc, HD ** -0.5, splits, po, pl, out_q8=att,
                                      counters=cnt),
+        rows * ctx * NKV * HD * 2 * 2)
+    cases["attention_scratch"] = (
+        lambda i: ops.attention_decode(q, kc, vc, tables, rs, rc, HD ** -0.5, old_splits, po, pl, out_q8=att,
+                                       counters=cnt, cluster=False),
         rows * ctx * NKV * HD * 2 * 2)
 
     if only is not None and "lm_head" not in only:

@@ -32,7 +32,7 @@ ext_modules = [
     Extension(
         "hawking_b200._native",
         sources=_sources("native/*.cpp", "bindings/native_module.cpp", "bindings/formats_bindings.cpp",
-                         "bindings/engine_bindings.cpp"),
+                         "bindings/engine_bindings.cpp", "bindings/serve_bindings.cpp"),
         include_dirs=[pybind11.get_include(), os.path.join(ROOT, CSRC)],
         extra_compile_args=CXX_FLAGS,
         extra_link_args=["-pthread"],

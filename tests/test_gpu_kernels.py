@@ -132,7 +132,7 @@ def _paged_attention_ref(q, kc, vc, tables, row_seq, row_ctx, scale):
 
 
 @pytest.mark.parametrize("nh,nkv,hd", [(8, 2, 64), (32, 8, 128), (16, 2, 256), (8, 8, 128)])
-@pytest.mark.parametrize("splits", [1, 7])
+@pytest.mark.parametrize("splits", [1, 2, 8, 7])  # 1/2/8: cluster (DSMEM) merge, 7: scratch + counters
 def test_attention_decode(nh, nkv, hd, splits):
     g = torch.Generator(device=DEV).manual_seed(nh + hd + splits)
     bs, nblk = 16, 40
