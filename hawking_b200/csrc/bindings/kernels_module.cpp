@@ -40,7 +40,7 @@ void gemv(int64_t fmt, int64_t epi, const std::vector<Tensor>& w0, const std::ve
           int64_t K, const optional<Tensor>& xq_, const optional<Tensor>& xd_, const optional<Tensor>& xs_,
           const optional<Tensor>& y, const optional<Tensor>& bias, const optional<Tensor>& oq,
           const optional<Tensor>& od, const optional<Tensor>& os, const optional<Tensor>& x_f32,
-          const optional<Tensor>& norm_w, double eps, bool pdl) {
+          const optional<Tensor>& norm_w, double eps, bool pdl, const optional<Tensor>& argmax_slots) {
   hk::GemvArgs a{};
   int nb;
   if (x_f32.has_value()) {
@@ -80,6 +80,12 @@ void gemv(int64_t fmt, int64_t epi, const std::vector<Tensor>& w0, const std::ve
     a.y_stride = y->stride(0);
   }
   a.bias = optr<float>(bias);
+  if (argmax_slots.has_value()) {
+    TORCH_CHECK(epi == hk::EPI_STORE, "gemv: argmax fusion needs the STORE epilogue");
+    TORCH_CHECK(argmax_slots->scalar_type() == at::kLong && argmax_slots->numel() >= (int64_t)nb * hk::kArgmaxSlots,
+                "gemv: argmax slots must be int64 [nb, 256]");
+    a.argmax_slots = reinterpret_cast<unsigned long long*>(argmax_slots->data_ptr<int64_t>());
+  }
   if (epi == hk::EPI_SWIGLU_Q8) {
     TORCH_CHECK(oq.has_value() && od.has_value() && os.has_value(), "gemv swiglu: q8 outputs required");
     TORCH_CHECK(!w1.empty(), "gemv swiglu: up-projection planes required");
@@ -242,7 +248,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("xq"), py::arg("xd"), py::arg("xs"), py::arg("y") = py::none(), py::arg("bias") = py::none(),
         py::arg("oq") = py::none(), py::arg("od") = py::none(), py::arg("os") = py::none(),
         py::arg("x_f32") = py::none(), py::arg("norm_w") = py::none(), py::arg("eps") = -1.0,
-        py::arg("pdl") = false);
+        py::arg("pdl") = false, py::arg("argmax_slots") = py::none());
   m.def("rmsnorm_q8", &rmsnorm_q8, py::arg("x"), py::arg("w"), py::arg("eps"), py::arg("norm"), py::arg("xq"),
         py::arg("xd"), py::arg("xs"), py::arg("y") = py::none(), py::arg("pdl") = false);
   m.def("rmsnorm", &rmsnorm, py::arg("x"), py::arg("w"), py::arg("eps"), py::arg("yf") = py::none(),
@@ -266,6 +272,18 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("out_bf16") = py::none(), py::arg("counters") = py::none(), py::arg("pdl") = false,
         py::arg("cluster") = false);
   m.def("argmax", &argmax, py::arg("logits"), py::arg("out"), py::arg("pdl") = false);
+  m.def(
+      "argmax_finalize",
+      [](const Tensor& slots, int64_t rows, const Tensor& out, bool pdl) {
+        check_cuda(slots, "slots");
+        TORCH_CHECK(slots.scalar_type() == at::kLong && slots.numel() >= rows * hk::kArgmaxSlots,
+                    "argmax_finalize: slots must be int64 [rows, 256]");
+        TORCH_CHECK(out.scalar_type() == at::kInt && out.numel() >= rows, "argmax_finalize: int32 out");
+        const c10::cuda::CUDAGuard g(slots.device());
+        hk::argmax_finalize_launch(reinterpret_cast<unsigned long long*>(slots.data_ptr<int64_t>()), (int)rows,
+                                   ptr<int>(out), cur_stream(), pdl);
+      },
+      py::arg("slots"), py::arg("rows"), py::arg("out"), py::arg("pdl") = false);
   m.def("sample", &sample, py::arg("logits"), py::arg("temperature"), py::arg("top_k"), py::arg("top_p"),
         py::arg("rep_penalty"), py::arg("recent"), py::arg("uniforms"), py::arg("out"), py::arg("pdl") = false);
   m.def("embed", &embed, py::arg("fmt"), py::arg("table"), py::arg("ids"), py::arg("out"), py::arg("pdl") = false);

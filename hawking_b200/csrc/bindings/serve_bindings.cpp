@@ -1,8 +1,10 @@
-// Bindings for the serving host logic: tokenizer, streaming detokeniser.
+// Bindings for the serving host logic: tokenizer, streaming detokeniser, HTTP server.
 #include <pybind11/pybind11.h>
 #include <pybind11/stl.h>
 
 #include "../native/gguf.h"
+#include "../native/http_server.h"
+#include "../native/json.h"
 #include "../native/tokenizer.h"
 
 namespace py = pybind11;
@@ -51,4 +53,48 @@ void bind_serve(py::module_& m) {
       .def("flush", [](StreamDecoder& d) { return py::bytes(d.flush()); });
 
   m.def("pretokenize", &pretokenize, py::arg("text"), py::arg("pre") = "default");
+
+  py::class_<ServeOptions>(m, "ServeOptions")
+      .def(py::init<>())
+      .def_readwrite("host", &ServeOptions::host)
+      .def_readwrite("port", &ServeOptions::port)
+      .def_readwrite("model_id", &ServeOptions::model_id)
+      .def_readwrite("chat_template", &ServeOptions::chat_template)
+      .def_readwrite("max_queue", &ServeOptions::max_queue)
+      .def_readwrite("max_connections", &ServeOptions::max_connections)
+      .def_readwrite("default_max_tokens", &ServeOptions::default_max_tokens)
+      .def_readwrite("max_context", &ServeOptions::max_context)
+      .def_readwrite("request_timeout_s", &ServeOptions::request_timeout_s);
+
+  py::class_<ServeRequest>(m, "ServeRequest")
+      .def_readonly("id", &ServeRequest::id)
+      .def_readonly("kind", &ServeRequest::kind)
+      .def_readonly("prompt", &ServeRequest::prompt)
+      .def_readonly("inputs", &ServeRequest::inputs)
+      .def_readonly("max_tokens", &ServeRequest::max_tokens)
+      .def_readonly("temperature", &ServeRequest::temperature)
+      .def_readonly("top_p", &ServeRequest::top_p)
+      .def_readonly("top_k", &ServeRequest::top_k)
+      .def_readonly("repetition_penalty", &ServeRequest::repetition_penalty)
+      .def_readonly("seed", &ServeRequest::seed)
+      .def_readonly("stream", &ServeRequest::stream)
+      .def_readonly("stop_ids", &ServeRequest::stop_ids);
+
+  py::class_<HttpServer, std::shared_ptr<HttpServer>>(m, "HttpServer")
+      .def(py::init<ServeOptions, std::shared_ptr<Tokenizer>>(), py::arg("options"), py::arg("tokenizer"))
+      .def("start", &HttpServer::start)
+      .def("stop", &HttpServer::stop, py::call_guard<py::gil_scoped_release>())
+      .def_property_readonly("port", &HttpServer::port)
+      .def("poll", &HttpServer::poll, py::arg("timeout_ms") = 0, py::call_guard<py::gil_scoped_release>())
+      .def("push", &HttpServer::push, py::arg("id"), py::arg("tokens"), py::arg("finish") = 0,
+           py::call_guard<py::gil_scoped_release>())
+      .def("push_embeddings", &HttpServer::push_embeddings, py::call_guard<py::gil_scoped_release>())
+      .def("fail", &HttpServer::fail)
+      .def("take_cancelled", &HttpServer::take_cancelled)
+      .def("set_metric", &HttpServer::set_metric, py::arg("name"), py::arg("value"), py::arg("help") = "",
+           py::arg("counter") = false)
+      .def("stats", [](const HttpServer& s) { return s.stats().dump(); })
+      .def("render_chat", [](const HttpServer& s, const std::string& messages_json, const std::string& tmpl) {
+        return s.render_chat(Json::parse(messages_json), tmpl.empty() ? s.resolve_template() : tmpl);
+      }, py::arg("messages_json"), py::arg("template") = "");
 }

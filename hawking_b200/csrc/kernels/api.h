@@ -51,7 +51,12 @@ struct GemvArgs {
   const float* norm_w;
   float eps;
   int norm;
+  // Greedy fusion (STORE epilogue): every row's value is folded into packed (value, index) keys
+  // with atomicMax, kArgmaxSlots slots per batch column (spreads the contention);
+  // argmax_finalize_launch turns them into token ids and clears them for the next launch.
+  unsigned long long* argmax_slots;
 };
+constexpr int kArgmaxSlots = 256;
 
 void gemv_launch(int fmt, int epi, const GemvArgs& a, int nb, cudaStream_t s, bool pdl);
 
@@ -106,11 +111,16 @@ struct AttnDecodeArgs {
   const float* sinks;          // optional per-head attention sink logits [nh]
   __nv_bfloat16* out_bf16;     // optional [R, nh*hd] bf16 output (tensor-core GEMM path)
   int* counters;               // [R * nkv] zero-initialised split counters (scratch; reset after use)
+  int* status;                 // optional device status word (bounded-wait timeouts)
+  int stage_blocks;            // cluster path: KV blocks held in the shared ring (set by the launcher)
 };
 void attention_decode_launch(const AttnDecodeArgs& a, cudaStream_t s, bool pdl);
 // Cluster variant (num_splits in {1, 2, 4, 8}): the splits of one (row, kv head) merge through
 // distributed shared memory; part_o / part_lse / counters are not used.
 void attention_decode_cluster_launch(const AttnDecodeArgs& a, cudaStream_t s, bool pdl);
+
+// Reduce the packed argmax slots of `rows` batch columns to token ids and zero the slots.
+void argmax_finalize_launch(unsigned long long* slots, int rows, int* out, cudaStream_t s, bool pdl);
 
 // Greedy: index of the max logit per row (lowest index on ties).
 void argmax_launch(const float* logits, int64_t stride, int rows, int V, int* out, cudaStream_t s, bool pdl);

@@ -16,7 +16,9 @@
 // mha_decode_llama_b9430_fattn_{main,reduce}, multiseq variant with per-sequence regions);
 // CPU oracle crates/hawking-core/src/attn.rs:23 (mha_decode_step).
 #include "decode_ops.cuh"
+#include "sm100.cuh"
 
+#include <algorithm>
 #include <cooperative_groups.h>
 
 namespace cg = cooperative_groups;
@@ -278,15 +280,43 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnDecodeArgs a) {
 }
 
 // ---------------------------------------------------------------------------------------------
-// Cluster variant: the S = num_splits CTAs of one (row, kv head) form a thread-block cluster. CTA
-// s owns the s-th contiguous token range and its WARPS warps interleave over tiles of T tokens as
-// above. The warps' partials are folded into one (max, sum, o) per CTA in shared memory; after a
-// cluster barrier each CTA merges whole 32-dim output blocks across the S CTAs by reading their
-// shared memory directly (distributed shared memory) and writes them. No global scratch, no split
-// counters, no second pass over memory.
+// Cluster variant: the S = num_splits CTAs of one (row, kv head) form a thread-block cluster; CTA s
+// owns the s-th contiguous token range (a whole number of KV blocks). One thread streams the
+// range's K and V block slabs (block_size x head_dim bf16, contiguous per head) into shared
+// memory with untiled bulk async copies completing on an mbarrier: every byte of the window is in
+// flight at once (one memory round trip), and when the range exceeds the shared ring it is
+// processed in two alternating windows (the next window loads while this one is computed). The
+// WARPS warps then take tiles of T tokens from shared memory (lane = HPL dims of every head of the
+// group; transpose-butterfly score reduction; online softmax). The warps' partials are folded into
+// one (max, sum, o) per CTA; after a cluster barrier each CTA merges whole 32-dim output blocks
+// across the S CTAs by reading their shared memory directly (distributed shared memory). No
+// global scratch, no split counters, no second pass over memory.
+template <int HPL>
+__device__ __forceinline__ void lds_bf16(const __nv_bfloat16* p, float (&v)[HPL]) {
+  if constexpr (HPL == 2) {
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(p);
+    v[0] = __uint_as_float(w << 16);
+    v[1] = __uint_as_float(w & 0xFFFF0000u);
+  } else if constexpr (HPL == 4) {
+    const uint2 w = *reinterpret_cast<const uint2*>(p);
+    v[0] = __uint_as_float(w.x << 16);
+    v[1] = __uint_as_float(w.x & 0xFFFF0000u);
+    v[2] = __uint_as_float(w.y << 16);
+    v[3] = __uint_as_float(w.y & 0xFFFF0000u);
+  } else {
+    const uint4 w = *reinterpret_cast<const uint4*>(p);
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      v[2 * i] = __uint_as_float(ws[i] << 16);
+      v[2 * i + 1] = __uint_as_float(ws[i] & 0xFFFF0000u);
+    }
+  }
+}
+
 template <int G, int HPL, int WARPS>
 __global__ void __launch_bounds__(WARPS * 32) attn_decode_cluster_kernel(AttnDecodeArgs a) {
-  constexpr int T = (32 / G) > (HPL >= 8 ? 4 : 8) ? (HPL >= 8 ? 4 : 8) : (32 / G);
+  constexpr int T = (32 / G) > 8 ? 8 : (32 / G);
   constexpr int NV = G * T;
   constexpr int HD = HPL * 32;
   cg::cluster_group cluster = cg::this_cluster();
@@ -294,17 +324,51 @@ __global__ void __launch_bounds__(WARPS * 32) attn_decode_cluster_kernel(AttnDec
   const int split = (int)cluster.block_rank();
   const int kvh = blockIdx.y, r = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  extern __shared__ __align__(128) uint8_t att_smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(att_smem);  // [2] window barriers
+  __nv_bfloat16* ring = reinterpret_cast<__nv_bfloat16*>(att_smem + 128);
   __shared__ float s_wm[WARPS][G];
   __shared__ float s_m[G], s_l[G];
   __shared__ __align__(16) float s_o[G][HD];
   for (int i = threadIdx.x; i < G * HD; i += blockDim.x) (&s_o[0][0])[i] = 0.f;
   if (threadIdx.x < G) s_l[threadIdx.x] = 0.f;
+  if (threadIdx.x == 0) {
+    sm100::mbar_init(&full[0], 1);
+    sm100::mbar_init(&full[1], 1);
+    sm100::fence_barrier_init();
+  }
+  __syncthreads();
 
   pdl_wait();
+  const int bs = a.block_size;
+  const int slab = bs * HD;  // elements of one head's K (or V) in one block
   const int ctx = a.row_ctx[r];
   const int* btab = a.block_tables + (int64_t)a.row_seq[r] * a.max_blocks;
-  const int chunk = ((ctx + S - 1) / S + T - 1) / T * T;
-  const int t0 = split * chunk, t1 = min(ctx, t0 + chunk);
+  const int nblk_ctx = (ctx + bs - 1) / bs;
+  const int bpc = (nblk_ctx + S - 1) / S;  // blocks per CTA
+  const int b0 = split * bpc, b1 = min(nblk_ctx, b0 + bpc);
+  const int t0 = b0 * bs, t1 = min(ctx, b1 * bs);
+  const int nb = max(0, b1 - b0);
+  const int NS = a.stage_blocks;
+  const bool dbl = nb > NS;
+  const int WB = dbl ? NS / 2 : NS;
+  const int nwin = nb > 0 ? (nb + WB - 1) / WB : 0;
+
+  auto issue = [&](int w) {  // thread 0: bulk-copy window w's K/V slabs into its ring half
+    const int buf = dbl ? (w & 1) : 0;
+    const int wb0 = b0 + w * WB, wb1 = min(b1, wb0 + WB);
+    sm100::mbar_arrive_expect_tx(&full[buf], (uint32_t)((wb1 - wb0) * 2 * slab * 2));
+    for (int b = wb0; b < wb1; ++b) {
+      const int64_t src = ((int64_t)btab[b] * a.nkv + kvh) * slab;
+      __nv_bfloat16* dst = ring + (int64_t)(buf * WB + (b - wb0)) * 2 * slab;
+      sm100::bulk_g2s(dst, a.k_cache + src, (uint32_t)slab * 2, &full[buf]);
+      sm100::bulk_g2s(dst + slab, a.v_cache + src, (uint32_t)slab * 2, &full[buf]);
+    }
+  };
+  if (threadIdx.x == 0 && nwin > 0) {
+    issue(0);
+    if (dbl && nwin > 1) issue(1);
+  }
 
   float q[G][HPL];
 #pragma unroll
@@ -321,85 +385,92 @@ __global__ void __launch_bounds__(WARPS * 32) attn_decode_cluster_kernel(AttnDec
 #pragma unroll
     for (int i = 0; i < HPL; ++i) acc[g][i] = 0.f;
   }
-  const int bs = a.block_size;
-  const int64_t head_stride = (int64_t)bs * HD;
-  for (int tt = t0 + warp * T; tt < t1; tt += WARPS * T) {
-    const int blk_a = btab[tt / bs];
-    const int blk_b = btab[min(tt + T - 1, t1 - 1) / bs];
-    float kreg[T][HPL], vreg[T][HPL];
-#pragma unroll
-    for (int j = 0; j < T; ++j) {
-      const int t = tt + j;
-      if (t < t1) {
-        const int blk = (t / bs == tt / bs) ? blk_a : blk_b;
-        const int64_t off = ((int64_t)blk * a.nkv + kvh) * head_stride + (int64_t)(t % bs) * HD + lane * HPL;
-        load_bf16<HPL>(a.k_cache + off, kreg[j]);
-        load_bf16<HPL>(a.v_cache + off, vreg[j]);
-      } else {
-#pragma unroll
-        for (int i = 0; i < HPL; ++i) { kreg[j][i] = 0.f; vreg[j][i] = 0.f; }
+  bool ok = true;
+  for (int w = 0; w < nwin; ++w) {
+    const int buf = dbl ? (w & 1) : 0;
+    const uint32_t parity = (uint32_t)((dbl ? (w >> 1) : w) & 1);
+    if (ok) {
+      ok = sm100::mbar_wait(&full[buf], parity, a.status);
+      if (!ok && threadIdx.x == 0) {  // timed out: give this window's copies one more bounded wait
+        for (uint32_t i = 0; i < (1u << 20) && !sm100::mbar_try_wait(&full[buf], parity); ++i) {
+        }
       }
     }
-    float part[32];
+    const int wb0 = b0 + w * WB;
+    const int tw0 = max(t0, wb0 * bs), tw1 = min(t1, min(b1, wb0 + WB) * bs);
+    const __nv_bfloat16* base = ring + (int64_t)buf * WB * 2 * slab;
+    for (int tt = tw0 + warp * T; ok && tt < tw1; tt += WARPS * T) {
+      float part[32];
 #pragma unroll
-    for (int v = NV; v < 32; ++v) part[v] = 0.f;
+      for (int v = NV; v < 32; ++v) part[v] = 0.f;
 #pragma unroll
-    for (int j = 0; j < T; ++j) {
+      for (int j = 0; j < T; ++j) {
+        const int t = min(tt + j, tw1 - 1);
+        const int lb = t / bs - wb0;
+        float kr[HPL];
+        lds_bf16<HPL>(base + (int64_t)lb * 2 * slab + (t % bs) * HD + lane * HPL, kr);
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          float sdot = 0.f;
+#pragma unroll
+          for (int i = 0; i < HPL; ++i) sdot = fmaf(q[g][i], kr[i], sdot);
+          part[g * T + j] = sdot;
+        }
+      }
+#pragma unroll
+      for (int o = 16, n = 32; o > 0; o >>= 1, n >>= 1) {
+        const bool up = lane & o;
+#pragma unroll
+        for (int i = 0; i < n / 2; ++i) {
+          const float send = up ? part[i] : part[i + n / 2];
+          const float keep = up ? part[i + n / 2] : part[i];
+          part[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+      }
+      const int my_g = min(lane / T, G - 1), my_j = lane % T;
+      const float score = (lane < NV && tt + my_j < tw1) ? part[0] : -INFINITY;
+      float tmax = score;
+#pragma unroll
+      for (int o = T / 2; o > 0; o >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
+      float p_new_m[G], alpha[G];
 #pragma unroll
       for (int g = 0; g < G; ++g) {
-        float sdot = 0.f;
-#pragma unroll
-        for (int i = 0; i < HPL; ++i) sdot = fmaf(q[g][i], kreg[j][i], sdot);
-        part[g * T + j] = sdot;
+        const float tm = __shfl_sync(0xffffffffu, tmax, g * T);
+        p_new_m[g] = fmaxf(m[g], tm);
+        alpha[g] = __expf(m[g] - p_new_m[g]);
       }
-    }
+      float mg = p_new_m[0];
 #pragma unroll
-    for (int o = 16, n = 32; o > 0; o >>= 1, n >>= 1) {
-      const bool up = lane & o;
+      for (int g = 1; g < G; ++g)
+        if (my_g == g) mg = p_new_m[g];
+      const float p = (score == -INFINITY) ? 0.f : __expf(score - mg);
+      float psum = p;
 #pragma unroll
-      for (int i = 0; i < n / 2; ++i) {
-        const float send = up ? part[i] : part[i + n / 2];
-        const float keep = up ? part[i + n / 2] : part[i];
-        part[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-      }
-    }
-    const int my_g = min(lane / T, G - 1), my_j = lane % T;
-    const float score = (lane < NV && tt + my_j < t1) ? part[0] : -INFINITY;
-    float tmax = score;
-#pragma unroll
-    for (int o = T / 2; o > 0; o >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
-    float p_new_m[G], alpha[G];
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const float tm = __shfl_sync(0xffffffffu, tmax, g * T);
-      p_new_m[g] = fmaxf(m[g], tm);
-      alpha[g] = __expf(m[g] - p_new_m[g]);
-    }
-    float mg = p_new_m[0];
-#pragma unroll
-    for (int g = 1; g < G; ++g)
-      if (my_g == g) mg = p_new_m[g];
-    const float p = (score == -INFINITY) ? 0.f : __expf(score - mg);
-    float psum = p;
-#pragma unroll
-    for (int o = T / 2; o > 0; o >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, o);
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const float ps = __shfl_sync(0xffffffffu, psum, g * T);
-      l[g] = l[g] * alpha[g] + ps;
-      m[g] = p_new_m[g];
-#pragma unroll
-      for (int i = 0; i < HPL; ++i) acc[g][i] *= alpha[g];
-    }
-#pragma unroll
-    for (int j = 0; j < T; ++j) {
+      for (int o = T / 2; o > 0; o >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, o);
 #pragma unroll
       for (int g = 0; g < G; ++g) {
-        const float pg = __shfl_sync(0xffffffffu, p, g * T + j);
+        const float ps = __shfl_sync(0xffffffffu, psum, g * T);
+        l[g] = l[g] * alpha[g] + ps;
+        m[g] = p_new_m[g];
 #pragma unroll
-        for (int i = 0; i < HPL; ++i) acc[g][i] = fmaf(pg, vreg[j][i], acc[g][i]);
+        for (int i = 0; i < HPL; ++i) acc[g][i] *= alpha[g];
+      }
+#pragma unroll
+      for (int j = 0; j < T; ++j) {
+        const int t = min(tt + j, tw1 - 1);
+        const int lb = t / bs - wb0;
+        float vr[HPL];
+        lds_bf16<HPL>(base + (int64_t)lb * 2 * slab + slab + (t % bs) * HD + lane * HPL, vr);
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float pg = __shfl_sync(0xffffffffu, p, g * T + j);
+#pragma unroll
+          for (int i = 0; i < HPL; ++i) acc[g][i] = fmaf(pg, vr[i], acc[g][i]);
+        }
       }
     }
+    __syncthreads();  // every warp is done with this ring half
+    if (threadIdx.x == 0 && dbl && w + 2 < nwin && ok) issue(w + 2);
   }
   // ---- fold the warps into one (m, l, o) per CTA ----
   if (lane == 0) {
@@ -430,13 +501,13 @@ __global__ void __launch_bounds__(WARPS * 32) attn_decode_cluster_kernel(AttnDec
   for (int blk = split + S * warp; blk < NBLK; blk += S * WARPS) {
     const int idx = blk * 32 + lane;
     const int g = idx / HD, d = idx % HD;
-    float mk[8], lk[8], ok[8];
+    float mk[8], lk[8], okv[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       if (k < S) {
         mk[k] = *cluster.map_shared_rank(&s_m[g], k);
         lk[k] = *cluster.map_shared_rank(&s_l[g], k);
-        ok[k] = *cluster.map_shared_rank(&s_o[g][d], k);
+        okv[k] = *cluster.map_shared_rank(&s_o[g][d], k);
       }
     }
     float M = -INFINITY;
@@ -451,7 +522,7 @@ __global__ void __launch_bounds__(WARPS * 32) attn_decode_cluster_kernel(AttnDec
       if (k < S && mk[k] != -INFINITY) {
         const float f = __expf(mk[k] - M);
         L += lk[k] * f;
-        O += ok[k] * f;
+        O += okv[k] * f;
       }
     }
     if (a.sinks) L += __expf(sink - M);
@@ -473,11 +544,25 @@ __global__ void __launch_bounds__(WARPS * 32) attn_decode_cluster_kernel(AttnDec
   cluster.sync();  // keep this CTA's shared memory alive until every CTA has read it
 }
 
+// Shared-memory ring: at most kAttnRingBytes of K/V slabs per CTA (enough blocks for the CTA's
+// largest possible token range, bounded by the block-table width).
+constexpr int kAttnRingBytes = 192 * 1024;
+
 template <int G, int HPL>
-static void launch_cluster_g(const AttnDecodeArgs& a, cudaStream_t s, bool pdl) {
+static void launch_cluster_g(AttnDecodeArgs a, cudaStream_t s, bool pdl) {
   constexpr int WARPS = G * HPL <= 16 ? 16 : 8;
-  launch_cluster(attn_decode_cluster_kernel<G, HPL, WARPS>, dim3(a.num_splits, a.nkv, a.R), dim3(WARPS * 32), 0,
-                 s, pdl, a.num_splits, a);
+  constexpr int HD = HPL * 32;
+  const int pair = 2 * a.block_size * HD * 2;  // K + V slab bytes of one block
+  const int most = (a.max_blocks + a.num_splits - 1) / a.num_splits;
+  int ns = std::min(most, kAttnRingBytes / pair);
+  if (ns < most && ns >= 2) ns &= ~1;  // two equal windows when the range does not fit at once
+  if (ns < 1 || (ns < most && ns < 2))
+    throw std::runtime_error("attention: KV block too large for the shared-memory ring");
+  a.stage_blocks = ns;
+  const size_t smem = 128 + (size_t)ns * pair;
+  auto kern = attn_decode_cluster_kernel<G, HPL, WARPS>;
+  HK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  launch_cluster(kern, dim3(a.num_splits, a.nkv, a.R), dim3(WARPS * 32), smem, s, pdl, a.num_splits, a);
 }
 
 template <int HPL>
@@ -496,6 +581,8 @@ static void launch_cluster_hpl(const AttnDecodeArgs& a, int G, cudaStream_t s, b
 
 void attention_decode_cluster_launch(const AttnDecodeArgs& a, cudaStream_t s, bool pdl) {
   if (a.nh % a.nkv) throw std::runtime_error("attention: n_heads must be a multiple of n_kv_heads");
+  if ((reinterpret_cast<uintptr_t>(a.k_cache) | reinterpret_cast<uintptr_t>(a.v_cache)) & 15)
+    throw std::runtime_error("attention (cluster): K/V caches must be 16-byte aligned");
   if (a.num_splits != 1 && a.num_splits != 2 && a.num_splits != 4 && a.num_splits != 8)
     throw std::runtime_error("attention (cluster): num_splits must be 1, 2, 4 or 8");
   const int G = a.nh / a.nkv;

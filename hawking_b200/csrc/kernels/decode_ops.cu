@@ -215,7 +215,31 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* logits, int64
   const float* l = logits + (int64_t)blockIdx.x * stride;
   float bv = -INFINITY;
   int bi = 0x7fffffff;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) argmax_merge(bv, bi, l[i], i);
+  const bool vec = ((reinterpret_cast<uintptr_t>(l) & 15) == 0);
+  const int V4 = vec ? V / 4 : 0;
+  // 4 independent 16-byte loads in flight per thread per iteration
+  int i = threadIdx.x;
+  for (; i + 3 * 1024 < V4; i += 4 * 1024) {
+    float4 x[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) x[u] = __ldg(reinterpret_cast<const float4*>(l) + i + u * 1024);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int b = 4 * (i + u * 1024);
+      argmax_merge(bv, bi, x[u].x, b);
+      argmax_merge(bv, bi, x[u].y, b + 1);
+      argmax_merge(bv, bi, x[u].z, b + 2);
+      argmax_merge(bv, bi, x[u].w, b + 3);
+    }
+  }
+  for (; i < V4; i += 1024) {
+    const float4 x = __ldg(reinterpret_cast<const float4*>(l) + i);
+    argmax_merge(bv, bi, x.x, 4 * i);
+    argmax_merge(bv, bi, x.y, 4 * i + 1);
+    argmax_merge(bv, bi, x.z, 4 * i + 2);
+    argmax_merge(bv, bi, x.w, 4 * i + 3);
+  }
+  for (int j = 4 * V4 + threadIdx.x; j < V; j += 1024) argmax_merge(bv, bi, l[j], j);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     float v2 = __shfl_xor_sync(0xffffffffu, bv, o);
@@ -240,8 +264,40 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* logits, int64
   pdl_launch();
 }
 
+
 void argmax_launch(const float* logits, int64_t stride, int rows, int V, int* out, cudaStream_t s, bool pdl) {
   launch(argmax_kernel, dim3(rows), dim3(1024), 0, s, pdl, logits, stride, V, out);
+}
+
+// One CTA per batch column: max over the packed slots, decode the index, clear the slots.
+__global__ void __launch_bounds__(256) argmax_finalize_kernel(unsigned long long* slots, int* out) {
+  pdl_wait();
+  unsigned long long* sl = slots + (int64_t)blockIdx.x * kArgmaxSlots;
+  unsigned long long best = 0;
+  for (int i = threadIdx.x; i < kArgmaxSlots; i += blockDim.x) {
+    const unsigned long long k = sl[i];
+    best = k > best ? k : best;
+    sl[i] = 0ull;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long k = __shfl_xor_sync(0xffffffffu, best, o);
+    best = k > best ? k : best;
+  }
+  __shared__ unsigned long long wbest[8];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  if (lane == 0) wbest[w] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int j = 1; j < (int)(blockDim.x >> 5); ++j) best = wbest[j] > best ? wbest[j] : best;
+    best = wbest[0] > best ? wbest[0] : best;
+    out[blockIdx.x] = best == 0ull ? 0 : (int)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFull));
+  }
+  pdl_launch();
+}
+
+void argmax_finalize_launch(unsigned long long* slots, int rows, int* out, cudaStream_t s, bool pdl) {
+  launch(argmax_finalize_kernel, dim3(rows), dim3(256), 0, s, pdl, slots, out);
 }
 
 // ---- sampling ---------------------------------------------------------------------------------

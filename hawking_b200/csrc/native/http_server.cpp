@@ -1,0 +1,684 @@
+// OpenAI-compatible HTTP/1.1 + SSE server; see http_server.h.
+#include "http_server.h"
+
+#include <arpa/inet.h>
+#include <netinet/in.h>
+#include <netinet/tcp.h>
+#include <poll.h>
+#include <sys/socket.h>
+#include <sys/time.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cstring>
+#include <sstream>
+#include <stdexcept>
+
+namespace hk {
+
+struct HttpServer::Pending {
+  uint64_t id = 0;
+  std::mutex mu;
+  std::condition_variable cv;
+  std::deque<int32_t> tokens;
+  int finish = 0;
+  bool done = false;
+  std::vector<std::vector<float>> emb;
+  bool emb_ready = false;
+  int err_status = 0;
+  std::string err_msg;
+};
+
+namespace {
+
+using Clock = std::chrono::steady_clock;
+
+const char* status_text(int s) {
+  switch (s) {
+    case 200: return "OK";
+    case 400: return "Bad Request";
+    case 404: return "Not Found";
+    case 405: return "Method Not Allowed";
+    case 413: return "Payload Too Large";
+    case 500: return "Internal Server Error";
+    case 501: return "Not Implemented";
+    case 503: return "Service Unavailable";
+    case 504: return "Gateway Timeout";
+    default: return "Error";
+  }
+}
+
+bool write_all(int fd, const std::string& s) {
+  size_t off = 0;
+  while (off < s.size()) {
+    const ssize_t n = ::send(fd, s.data() + off, s.size() - off, MSG_NOSIGNAL);
+    if (n <= 0) return false;
+    off += (size_t)n;
+  }
+  return true;
+}
+
+bool respond(int fd, int status, const std::string& ctype, const std::string& body, bool keep_alive) {
+  std::ostringstream h;
+  h << "HTTP/1.1 " << status << ' ' << status_text(status) << "\r\n"
+    << "Content-Type: " << ctype << "\r\n"
+    << "Content-Length: " << body.size() << "\r\n"
+    << "Connection: " << (keep_alive ? "keep-alive" : "close") << "\r\n\r\n";
+  return write_all(fd, h.str() + body);
+}
+
+std::string error_body(const std::string& message, const std::string& type, const std::string& code) {
+  Json e = Json::object();
+  e.set("message", Json::string(message));
+  e.set("type", Json::string(type));
+  e.set("code", Json::string(code));
+  Json o = Json::object();
+  o.set("error", e);
+  return o.dump();
+}
+
+bool respond_error(int fd, int status, const std::string& message, const std::string& code, bool keep_alive) {
+  const std::string type = status >= 500 ? (status == 501 ? "not_implemented" : "internal_error")
+                                         : "invalid_request_error";
+  return respond(fd, status, "application/json", error_body(message, type, code), keep_alive);
+}
+
+std::string lower(std::string s) {
+  for (auto& c : s) c = (char)std::tolower((unsigned char)c);
+  return s;
+}
+
+// Text of an OpenAI message "content": a string, or an array of {"type":"text","text":...} parts.
+std::string content_text(const Json& c) {
+  if (c.is_string()) return c.as_string();
+  std::string out;
+  if (c.is_array())
+    for (const auto& p : c.items())
+      if (p.is_object() && p["text"].is_string()) out += p["text"].as_string();
+  return out;
+}
+
+double num_or(const Json& o, const char* k, double d) { return o.has(k) && o[k].is_number() ? o[k].as_double() : d; }
+
+// Longest suffix of `text` that is a proper prefix of some stop string (held back while streaming).
+size_t stop_holdback(const std::string& text, const std::vector<std::string>& stops) {
+  size_t hold = 0;
+  for (const auto& s : stops)
+    for (size_t k = std::min(s.size() - 1, text.size()); k > hold; --k)
+      if (text.compare(text.size() - k, k, s, 0, k) == 0) { hold = k; break; }
+  return hold;
+}
+
+std::string random_hex_id(uint64_t id) {
+  char buf[40];
+  snprintf(buf, sizeof buf, "%016llx", (unsigned long long)(id * 0x9E3779B97F4A7C15ull));
+  return buf;
+}
+
+}  // namespace
+
+HttpServer::HttpServer(ServeOptions opts, std::shared_ptr<Tokenizer> tok) : opts_(std::move(opts)), tok_(std::move(tok)) {
+  if (!tok_) throw std::runtime_error("http server: a tokenizer is required");
+}
+
+HttpServer::~HttpServer() { stop(); }
+
+void HttpServer::start() {
+  if (running_) return;
+  listen_fd_ = ::socket(AF_INET, SOCK_STREAM, 0);
+  if (listen_fd_ < 0) throw std::runtime_error("http server: socket() failed");
+  int one = 1;
+  setsockopt(listen_fd_, SOL_SOCKET, SO_REUSEADDR, &one, sizeof one);
+  sockaddr_in addr{};
+  addr.sin_family = AF_INET;
+  addr.sin_port = htons((uint16_t)opts_.port);
+  if (inet_pton(AF_INET, opts_.host.c_str(), &addr.sin_addr) != 1) {
+    ::close(listen_fd_);
+    throw std::runtime_error("http server: bad host " + opts_.host);
+  }
+  if (::bind(listen_fd_, (sockaddr*)&addr, sizeof addr) != 0 || ::listen(listen_fd_, 128) != 0) {
+    ::close(listen_fd_);
+    throw std::runtime_error("http server: cannot listen on " + opts_.host + ":" + std::to_string(opts_.port));
+  }
+  socklen_t len = sizeof addr;
+  getsockname(listen_fd_, (sockaddr*)&addr, &len);
+  bound_port_ = ntohs(addr.sin_port);
+  running_ = true;
+  accept_thread_ = std::thread([this] { accept_loop(); });
+}
+
+void HttpServer::stop() {
+  if (!running_.exchange(false)) return;
+  ::shutdown(listen_fd_, SHUT_RDWR);
+  ::close(listen_fd_);
+  if (accept_thread_.joinable()) accept_thread_.join();
+  std::vector<std::shared_ptr<Pending>> ps;
+  {
+    std::lock_guard<std::mutex> g(mu_);
+    for (auto& kv : pending_) ps.push_back(kv.second);
+    queue_.clear();
+  }
+  for (auto& p : ps) {
+    std::lock_guard<std::mutex> g(p->mu);
+    p->err_status = 503;
+    p->err_msg = "server shutting down";
+    p->done = true;
+    p->cv.notify_all();
+  }
+  cv_.notify_all();
+  // connection threads are detached; wait (bounded) for them to leave
+  for (int i = 0; i < 500 && connections_.load() > 0; ++i) std::this_thread::sleep_for(std::chrono::milliseconds(10));
+}
+
+void HttpServer::accept_loop() {
+  while (running_) {
+    pollfd p{listen_fd_, POLLIN, 0};
+    if (::poll(&p, 1, 100) <= 0) continue;
+    const int fd = ::accept(listen_fd_, nullptr, nullptr);
+    if (fd < 0) continue;
+    if (connections_.load() >= opts_.max_connections) {
+      respond_error(fd, 503, "too many connections", "overloaded", false);
+      ::close(fd);
+      continue;
+    }
+    int one = 1;
+    setsockopt(fd, IPPROTO_TCP, TCP_NODELAY, &one, sizeof one);
+    timeval tv{30, 0};
+    setsockopt(fd, SOL_SOCKET, SO_RCVTIMEO, &tv, sizeof tv);
+    connections_++;
+    std::thread([this, fd] {
+      try {
+        serve_connection(fd);
+      } catch (...) {
+      }
+      ::close(fd);
+      connections_--;
+    }).detach();
+  }
+}
+
+void HttpServer::serve_connection(int fd) {
+  std::string buf;
+  char tmp[8192];
+  while (running_) {
+    // ---- read the header block ----
+    size_t hend;
+    while ((hend = buf.find("\r\n\r\n")) == std::string::npos) {
+      if (buf.size() > (1 << 16)) { respond_error(fd, 413, "header too large", "header_too_large", false); return; }
+      const ssize_t n = ::recv(fd, tmp, sizeof tmp, 0);
+      if (n <= 0) return;
+      buf.append(tmp, (size_t)n);
+    }
+    const std::string head = buf.substr(0, hend);
+    buf.erase(0, hend + 4);
+    std::istringstream hs(head);
+    std::string method, target, version;
+    hs >> method >> target >> version;
+    size_t clen = 0;
+    bool keep_alive = version == "HTTP/1.1";
+    std::string line;
+    std::getline(hs, line);
+    while (std::getline(hs, line)) {
+      if (!line.empty() && line.back() == '\r') line.pop_back();
+      const size_t c = line.find(':');
+      if (c == std::string::npos) continue;
+      const std::string k = lower(line.substr(0, c));
+      std::string v = line.substr(c + 1);
+      v.erase(0, v.find_first_not_of(" \t"));
+      if (k == "content-length") clen = (size_t)std::strtoull(v.c_str(), nullptr, 10);
+      else if (k == "connection") keep_alive = lower(v) != "close";
+    }
+    if (clen > (64u << 20)) { respond_error(fd, 413, "body too large", "body_too_large", false); return; }
+    while (buf.size() < clen) {
+      const ssize_t n = ::recv(fd, tmp, sizeof tmp, 0);
+      if (n <= 0) return;
+      buf.append(tmp, (size_t)n);
+    }
+    const std::string body = buf.substr(0, clen);
+    buf.erase(0, clen);
+    const size_t q = target.find('?');
+    const std::string path = q == std::string::npos ? target : target.substr(0, q);
+    if (!handle(fd, method, path, body, keep_alive) || !keep_alive) return;
+  }
+}
+
+bool HttpServer::handle(int fd, const std::string& method, const std::string& path, const std::string& body,
+                        bool keep_alive) {
+  if (path == "/healthz" || path == "/health") {
+    if (method != "GET") return respond_error(fd, 405, "use GET", "method_not_allowed", keep_alive);
+    return respond(fd, 200, "text/plain", "ok", keep_alive);
+  }
+  if (path == "/metrics") return respond(fd, 200, "text/plain; version=0.0.4", metrics_text(), keep_alive);
+  if (path == "/v1/models") {
+    Json m = Json::object();
+    m.set("id", Json::string(opts_.model_id));
+    m.set("object", Json::string("model"));
+    m.set("owned_by", Json::string("hawking-b200"));
+    Json d = Json::array();
+    d.push(m);
+    Json o = Json::object();
+    o.set("object", Json::string("list"));
+    o.set("data", d);
+    return respond(fd, 200, "application/json", o.dump(), keep_alive);
+  }
+  if (path == "/v1/responses" || path == "/v1/messages") {
+    requests_rejected_++;
+    return respond(fd, 501, "application/json",
+                   error_body("POST " + path + " is not implemented by this server", "not_implemented",
+                              "not_implemented"),
+                   keep_alive);
+  }
+  const bool chat = path == "/v1/chat/completions", comp = path == "/v1/completions", emb = path == "/v1/embeddings";
+  if (!chat && !comp && !emb) return respond_error(fd, 404, "no route for " + path, "not_found", keep_alive);
+  if (method != "POST") return respond_error(fd, 405, "use POST", "method_not_allowed", keep_alive);
+  Json j;
+  try {
+    j = Json::parse(body);
+  } catch (const std::exception& e) {
+    return respond_error(fd, 400, std::string("request body is not valid JSON: ") + e.what(), "invalid_json",
+                         keep_alive);
+  }
+  if (!j.is_object()) return respond_error(fd, 400, "request body must be a JSON object", "invalid_json", keep_alive);
+  if (emb) return handle_embeddings(fd, j, keep_alive);
+  return handle_generate(fd, j, chat, keep_alive);
+}
+
+std::string HttpServer::resolve_template() const {
+  if (opts_.chat_template != "auto") return opts_.chat_template;
+  if (tok_->find("<|start_header_id|>") >= 0) return "llama3";
+  if (tok_->find("<|im_start|>") >= 0) return "chatml";
+  return "generic";
+}
+
+std::string HttpServer::render_chat(const Json& messages, const std::string& tmpl) const {
+  std::string out;
+  for (const auto& m : messages.items()) {
+    const std::string role = m["role"].is_string() ? m["role"].as_string() : "user";
+    const std::string text = content_text(m["content"]);
+    if (tmpl == "llama3") out += "<|start_header_id|>" + role + "<|end_header_id|>\n\n" + text + "<|eot_id|>";
+    else if (tmpl == "chatml") out += "<|im_start|>" + role + "\n" + text + "<|im_end|>\n";
+    else if (tmpl == "deepseek") {
+      if (role == "system") out += text + "\n\n";
+      else if (role == "assistant") out += "Assistant: " + text + "\n\n";
+      else out += "User: " + text + "\n\n";
+    } else out += role + ": " + text + "\n";
+  }
+  if (tmpl == "llama3") out += "<|start_header_id|>assistant<|end_header_id|>\n\n";
+  else if (tmpl == "chatml") out += "<|im_start|>assistant\n";
+  else if (tmpl == "deepseek") out += "Assistant:";
+  else out += "assistant:";
+  return out;
+}
+
+std::shared_ptr<HttpServer::Pending> HttpServer::admit(ServeRequest req) {
+  auto p = std::make_shared<Pending>();
+  std::lock_guard<std::mutex> g(mu_);
+  if ((int)queue_.size() >= opts_.max_queue) return nullptr;
+  req.id = next_id_++;
+  p->id = req.id;
+  pending_[req.id] = p;
+  prompt_tokens_ += req.prompt.size();
+  for (const auto& in : req.inputs) prompt_tokens_ += in.size();
+  queue_.push_back(std::move(req));
+  requests_admitted_++;
+  cv_.notify_one();
+  return p;
+}
+
+void HttpServer::forget(uint64_t id) {
+  std::lock_guard<std::mutex> g(mu_);
+  pending_.erase(id);
+}
+
+bool HttpServer::handle_generate(int fd, const Json& j, bool chat, bool keep_alive) {
+  ServeRequest r;
+  r.kind = chat ? "chat" : "completion";
+  std::string prompt_text;
+  if (chat) {
+    if (!j["messages"].is_array()) return respond_error(fd, 400, "'messages' must be an array", "invalid_json", keep_alive);
+    if (j["messages"].size() == 0)
+      return respond_error(fd, 400, "'messages' must not be empty", "missing_required_parameter", keep_alive);
+    prompt_text = render_chat(j["messages"], resolve_template());
+  } else {
+    const Json& p = j["prompt"];
+    if (p.is_string()) prompt_text = p.as_string();
+    else if (p.is_array() && p.size() > 0 && p.at(0).is_string()) prompt_text = p.at(0).as_string();
+    else if (!(p.is_array() && p.size() > 0 && p.at(0).is_number()))
+      return respond_error(fd, 400, "'prompt' must be a string or a token-id array", "missing_required_parameter",
+                           keep_alive);
+    if (p.is_array() && p.size() > 0 && p.at(0).is_number())
+      for (const auto& t : p.items()) r.prompt.push_back((int32_t)t.as_int());
+  }
+  if (r.prompt.empty()) r.prompt = tok_->encode(prompt_text, true);
+  if (r.prompt.empty()) return respond_error(fd, 400, "prompt tokenizes to nothing", "missing_required_parameter", keep_alive);
+  for (int32_t t : r.prompt)
+    if (t < 0 || (size_t)t >= tok_->vocab_size())
+      return respond_error(fd, 400, "token id out of range", "invalid_json", keep_alive);
+  r.max_tokens = (int)num_or(j, "max_completion_tokens", num_or(j, "max_tokens", opts_.default_max_tokens));
+  if (r.max_tokens <= 0) return respond_error(fd, 400, "'max_tokens' must be positive", "invalid_json", keep_alive);
+  if ((int)r.prompt.size() + r.max_tokens > opts_.max_context)
+    r.max_tokens = std::max(1, opts_.max_context - (int)r.prompt.size());
+  if ((int)r.prompt.size() >= opts_.max_context)
+    return respond_error(fd, 400, "prompt longer than the context window", "context_length_exceeded", keep_alive);
+  r.temperature = (float)num_or(j, "temperature", 1.0);
+  r.top_p = (float)num_or(j, "top_p", 1.0);
+  r.top_k = (int)num_or(j, "top_k", 0);
+  r.repetition_penalty = (float)num_or(j, "repetition_penalty", 1.0);
+  r.seed = (uint64_t)num_or(j, "seed", 42);
+  r.stream = j["stream"].type() == Json::Type::Bool && j["stream"].as_bool();
+  r.stop_ids = tok_->eog_ids();
+  std::vector<std::string> stops;
+  if (j["stop"].is_string()) stops.push_back(j["stop"].as_string());
+  else if (j["stop"].is_array())
+    for (const auto& s : j["stop"].items())
+      if (s.is_string() && !s.as_string().empty()) stops.push_back(s.as_string());
+  const size_t n_prompt = r.prompt.size();
+  const bool stream = r.stream;
+  auto p = admit(std::move(r));
+  if (!p) {
+    requests_rejected_++;
+    return respond_error(fd, 503, "request queue is full", "overloaded", keep_alive);
+  }
+  const uint64_t id = p->id;
+  const std::string oid = (chat ? "chatcmpl-" : "cmpl-") + random_hex_id(id);
+  const int64_t created = (int64_t)std::chrono::duration_cast<std::chrono::seconds>(
+                              std::chrono::system_clock::now().time_since_epoch()).count();
+  StreamDecoder dec(tok_.get());
+  std::string text, sent_upto_text;
+  size_t sent = 0, n_gen = 0;
+  std::string finish_reason;
+  bool stopped_by_string = false, client_gone = false;
+
+  auto chunk_json = [&](const std::string& delta, const std::string& fin, bool first) {
+    Json c = Json::object();
+    c.set("id", Json::string(oid));
+    c.set("object", Json::string(chat ? "chat.completion.chunk" : "text_completion"));
+    c.set("created", Json::integer(created));
+    c.set("model", Json::string(opts_.model_id));
+    Json ch = Json::object();
+    ch.set("index", Json::integer(0));
+    if (chat) {
+      Json d = Json::object();
+      if (first) d.set("role", Json::string("assistant"));
+      if (!delta.empty() || fin.empty()) d.set("content", Json::string(delta));
+      ch.set("delta", d);
+    } else {
+      ch.set("text", Json::string(delta));
+    }
+    ch.set("finish_reason", fin.empty() ? Json::null() : Json::string(fin));
+    Json arr = Json::array();
+    arr.push(ch);
+    c.set("choices", arr);
+    return "data: " + c.dump() + "\n\n";
+  };
+
+  if (stream) {
+    const std::string h =
+        "HTTP/1.1 200 OK\r\nContent-Type: text/event-stream\r\nCache-Control: no-cache\r\nConnection: close\r\n\r\n";
+    if (!write_all(fd, h)) client_gone = true;
+  }
+  bool first = true;
+  const auto deadline = Clock::now() + std::chrono::milliseconds((int64_t)(opts_.request_timeout_s * 1000));
+  while (!client_gone) {
+    std::deque<int32_t> toks;
+    int fin = 0;
+    bool done = false;
+    int err = 0;
+    std::string err_msg;
+    {
+      std::unique_lock<std::mutex> g(p->mu);
+      p->cv.wait_until(g, deadline, [&] { return !p->tokens.empty() || p->done; });
+      toks.swap(p->tokens);
+      fin = p->finish;
+      done = p->done;
+      err = p->err_status;
+      err_msg = p->err_msg;
+    }
+    if (err) {
+      forget(id);
+      if (stream) {
+        write_all(fd, "data: " + error_body(err_msg, "internal_error", "internal_error") + "\n\ndata: [DONE]\n\n");
+        return false;
+      }
+      return respond_error(fd, err, err_msg, err == 503 ? "overloaded" : "internal_error", keep_alive);
+    }
+    if (toks.empty() && !done) {  // timed out
+      forget(id);
+      {
+        std::lock_guard<std::mutex> g(mu_);
+        cancelled_.push_back(id);
+      }
+      if (stream) return false;
+      return respond_error(fd, 504, "generation timed out", "timeout", keep_alive);
+    }
+    for (int32_t t : toks) {
+      n_gen++;
+      tokens_generated_++;
+      if (tok_->is_eog(t)) continue;
+      text += dec.push(t);
+    }
+    if (done) text += dec.flush();
+    // stop strings
+    for (const auto& s : stops) {
+      const size_t at = text.find(s, sent > s.size() ? sent - s.size() : 0);
+      if (at != std::string::npos) {
+        text.resize(at);
+        stopped_by_string = true;
+      }
+    }
+    if (stopped_by_string) {
+      done = true;
+      fin = 2;
+    }
+    if (done) finish_reason = fin == 1 ? "length" : "stop";
+    if (stream) {
+      const size_t hold = done ? 0 : stop_holdback(text, stops);
+      const size_t upto = text.size() - std::min(hold, text.size() - sent);
+      if (upto > sent || first) {
+        const std::string delta = text.substr(sent, upto - sent);
+        if ((!delta.empty() || first) && !write_all(fd, chunk_json(delta, "", first))) client_gone = true;
+        first = false;
+        sent = upto;
+      }
+      if (done && !client_gone) {
+        write_all(fd, chunk_json("", finish_reason, false));
+        write_all(fd, "data: [DONE]\n\n");
+      }
+    }
+    if (done) break;
+  }
+  forget(id);
+  if (client_gone || stopped_by_string) {
+    std::lock_guard<std::mutex> g(mu_);
+    cancelled_.push_back(id);
+  }
+  requests_finished_++;
+  if (stream || client_gone) return false;
+  Json o = Json::object();
+  o.set("id", Json::string(oid));
+  o.set("object", Json::string(chat ? "chat.completion" : "text_completion"));
+  o.set("created", Json::integer(created));
+  o.set("model", Json::string(opts_.model_id));
+  Json ch = Json::object();
+  ch.set("index", Json::integer(0));
+  if (chat) {
+    Json msg = Json::object();
+    msg.set("role", Json::string("assistant"));
+    msg.set("content", Json::string(text));
+    ch.set("message", msg);
+  } else {
+    ch.set("text", Json::string(text));
+  }
+  ch.set("finish_reason", Json::string(finish_reason));
+  Json arr = Json::array();
+  arr.push(ch);
+  o.set("choices", arr);
+  Json u = Json::object();
+  u.set("prompt_tokens", Json::integer((int64_t)n_prompt));
+  u.set("completion_tokens", Json::integer((int64_t)n_gen));
+  u.set("total_tokens", Json::integer((int64_t)(n_prompt + n_gen)));
+  o.set("usage", u);
+  return respond(fd, 200, "application/json", o.dump(), keep_alive);
+}
+
+bool HttpServer::handle_embeddings(int fd, const Json& j, bool keep_alive) {
+  ServeRequest r;
+  r.kind = "embedding";
+  std::vector<std::string> inputs;
+  if (j["input"].is_string()) inputs.push_back(j["input"].as_string());
+  else if (j["input"].is_array())
+    for (const auto& s : j["input"].items())
+      if (s.is_string()) inputs.push_back(s.as_string());
+  if (inputs.empty()) return respond_error(fd, 400, "'input' must not be empty", "missing_required_parameter", keep_alive);
+  if (j.has("encoding_format") && j["encoding_format"].is_string() && j["encoding_format"].as_string() != "float")
+    return respond_error(fd, 400, "only encoding_format=float is supported", "invalid_json", keep_alive);
+  size_t n_tok = 0;
+  for (const auto& s : inputs) {
+    r.inputs.push_back(tok_->encode(s, true));
+    if (r.inputs.back().empty()) return respond_error(fd, 400, "input tokenizes to nothing", "missing_required_parameter", keep_alive);
+    if ((int)r.inputs.back().size() >= opts_.max_context)
+      return respond_error(fd, 400, "input longer than the context window", "context_length_exceeded", keep_alive);
+    n_tok += r.inputs.back().size();
+  }
+  auto p = admit(std::move(r));
+  if (!p) return respond_error(fd, 503, "request queue is full", "overloaded", keep_alive);
+  std::vector<std::vector<float>> vecs;
+  {
+    std::unique_lock<std::mutex> g(p->mu);
+    const bool ok = p->cv.wait_for(g, std::chrono::milliseconds((int64_t)(opts_.request_timeout_s * 1000)),
+                                   [&] { return p->emb_ready || p->done; });
+    if (!ok || p->err_status || !p->emb_ready) {
+      const int st = p->err_status ? p->err_status : 504;
+      const std::string msg = p->err_status ? p->err_msg : "embedding timed out";
+      g.unlock();
+      forget(p->id);
+      return respond_error(fd, st, msg, "internal_error", keep_alive);
+    }
+    vecs.swap(p->emb);
+  }
+  forget(p->id);
+  requests_finished_++;
+  Json data = Json::array();
+  for (size_t i = 0; i < vecs.size(); ++i) {
+    Json e = Json::object();
+    e.set("object", Json::string("embedding"));
+    e.set("index", Json::integer((int64_t)i));
+    Json v = Json::array();
+    for (float x : vecs[i]) v.push(Json::number(x));
+    e.set("embedding", v);
+    data.push(e);
+  }
+  Json o = Json::object();
+  o.set("object", Json::string("list"));
+  o.set("data", data);
+  o.set("model", Json::string(opts_.model_id));
+  Json u = Json::object();
+  u.set("prompt_tokens", Json::integer((int64_t)n_tok));
+  u.set("total_tokens", Json::integer((int64_t)n_tok));
+  o.set("usage", u);
+  return respond(fd, 200, "application/json", o.dump(), keep_alive);
+}
+
+std::vector<ServeRequest> HttpServer::poll(int timeout_ms) {
+  std::unique_lock<std::mutex> g(mu_);
+  if (queue_.empty() && timeout_ms > 0)
+    cv_.wait_for(g, std::chrono::milliseconds(timeout_ms), [&] { return !queue_.empty() || !running_; });
+  std::vector<ServeRequest> out(std::make_move_iterator(queue_.begin()), std::make_move_iterator(queue_.end()));
+  queue_.clear();
+  return out;
+}
+
+void HttpServer::push(uint64_t id, const std::vector<int32_t>& tokens, int finish) {
+  std::shared_ptr<Pending> p;
+  {
+    std::lock_guard<std::mutex> g(mu_);
+    auto it = pending_.find(id);
+    if (it == pending_.end()) return;
+    p = it->second;
+  }
+  std::lock_guard<std::mutex> g(p->mu);
+  p->tokens.insert(p->tokens.end(), tokens.begin(), tokens.end());
+  if (finish) {
+    p->finish = finish;
+    p->done = true;
+  }
+  p->cv.notify_all();
+}
+
+void HttpServer::push_embeddings(uint64_t id, const std::vector<std::vector<float>>& vecs) {
+  std::shared_ptr<Pending> p;
+  {
+    std::lock_guard<std::mutex> g(mu_);
+    auto it = pending_.find(id);
+    if (it == pending_.end()) return;
+    p = it->second;
+  }
+  std::lock_guard<std::mutex> g(p->mu);
+  p->emb = vecs;
+  p->emb_ready = true;
+  p->cv.notify_all();
+}
+
+void HttpServer::fail(uint64_t id, int status, const std::string& message) {
+  std::shared_ptr<Pending> p;
+  {
+    std::lock_guard<std::mutex> g(mu_);
+    auto it = pending_.find(id);
+    if (it == pending_.end()) return;
+    p = it->second;
+  }
+  std::lock_guard<std::mutex> g(p->mu);
+  p->err_status = status;
+  p->err_msg = message;
+  p->done = true;
+  p->cv.notify_all();
+}
+
+std::vector<uint64_t> HttpServer::take_cancelled() {
+  std::lock_guard<std::mutex> g(mu_);
+  std::vector<uint64_t> out;
+  out.swap(cancelled_);
+  return out;
+}
+
+void HttpServer::set_metric(const std::string& name, double value, const std::string& help, bool counter) {
+  std::lock_guard<std::mutex> g(mu_);
+  metrics_[name] = {value, {help, counter}};
+}
+
+std::string HttpServer::metrics_text() const {
+  std::ostringstream o;
+  auto emit = [&](const std::string& name, double v, const std::string& help, bool counter) {
+    o << "# HELP " << name << ' ' << help << "\n# TYPE " << name << ' ' << (counter ? "counter" : "gauge") << '\n'
+      << name << ' ' << json_number(v) << '\n';
+  };
+  size_t queued, active;
+  std::map<std::string, std::pair<double, std::pair<std::string, bool>>> extra;
+  {
+    std::lock_guard<std::mutex> g(mu_);
+    queued = queue_.size();
+    active = pending_.size() - std::min(pending_.size(), queued);
+    extra = metrics_;
+  }
+  emit("hawking_requests_admitted_total", (double)requests_admitted_, "Requests admitted to the engine queue", true);
+  emit("hawking_requests_finished_total", (double)requests_finished_, "Requests answered", true);
+  emit("hawking_requests_rejected_total", (double)requests_rejected_, "Requests refused (queue full or 501)", true);
+  emit("hawking_tokens_generated_total", (double)tokens_generated_, "Tokens generated across all requests", true);
+  emit("hawking_prompt_tokens_total", (double)prompt_tokens_, "Prompt tokens admitted", true);
+  emit("hawking_active_slots", (double)active, "Requests being generated", false);
+  emit("hawking_queued_requests", (double)queued, "Requests waiting for the engine loop", false);
+  for (const auto& kv : extra) emit(kv.first, kv.second.first, kv.second.second.first, kv.second.second.second);
+  return o.str();
+}
+
+Json HttpServer::stats() const {
+  Json o = Json::object();
+  o.set("requests_admitted", Json::uinteger(requests_admitted_));
+  o.set("requests_finished", Json::uinteger(requests_finished_));
+  o.set("tokens_generated", Json::uinteger(tokens_generated_));
+  o.set("connections", Json::integer(connections_.load()));
+  return o;
+}
+
+}  // namespace hk

@@ -227,6 +227,7 @@ class LlamaModel:
         self.top_p = torch.ones(R, device=self.dev)
         self.rep_penalty = torch.ones(R, device=self.dev)
         self.uniforms = torch.zeros(R, device=self.dev)
+        self.argmax_slots = torch.zeros(R, ops.ARGMAX_SLOTS, dtype=torch.int64, device=self.dev)
         self._graphs: Dict[tuple, torch.cuda.CUDAGraph] = {}
         self.launches_per_forward = 0
 
@@ -298,8 +299,13 @@ class LlamaModel:
                 xa = Q8Act.__new__(Q8Act)
                 xa.K, xa.q, xa.d, xa.s = self.xa.K, self.xa.q.index_select(0, idx), \
                     self.xa.d.index_select(0, idx), self.xa.s.index_select(0, idx)
+            fuse = sample == "greedy"
             self._gemv_cols(lambda c0, c1: ops.gemv(w.lm_head, self._q8_slice(xa, c0, c1, cfg.hidden),
-                                                    self.logits[c0:c1]), nl)
+                                                    self.logits[c0:c1],
+                                                    argmax_slots=self.argmax_slots[c0:c1] if fuse else None), nl)
+            if fuse:
+                ops.argmax_finalize(self.argmax_slots, nl, self.next_ids)
+                sample = "done"
         if sample == "greedy":
             ops.argmax(self.logits[:nl], self.next_ids[:nl])
         elif sample == "sample":

@@ -60,10 +60,21 @@ def rmsnorm(x, w, eps, yf=None, yb=None):
     kernels().rmsnorm(x, w, eps, yf, yb, PDL)
 
 
-def gemv(w: QWeight, x: Q8Act, y: torch.Tensor, residual: bool = False, bias=None):
+def gemv(w: QWeight, x: Q8Act, y: torch.Tensor, residual: bool = False, bias=None, argmax_slots=None):
+    """y[b] = W x[b] (or y += ... with ``residual``). ``argmax_slots`` (int64 [nb, 256], zeroed)
+    additionally folds every output into packed greedy keys; ``argmax_finalize`` reads them."""
     launches.add()
     kernels().gemv(w.fmt, EPI_RESID if residual else EPI_STORE, w.planes, [], w.N, w.K, x.q, x.d, x.s, y, bias,
-                   None, None, None, None, None, -1.0, PDL)
+                   None, None, None, None, None, -1.0, PDL, argmax_slots)
+
+
+ARGMAX_SLOTS = 256
+
+
+def argmax_finalize(slots: torch.Tensor, rows: int, out: torch.Tensor):
+    """Token ids from the packed greedy keys of a fused GEMV (lowest index on ties); clears them."""
+    launches.add()
+    kernels().argmax_finalize(slots, rows, out, PDL)
 
 
 def gemv_swiglu(w_gate: QWeight, w_up: QWeight, x: Q8Act, out: Q8Act):

@@ -158,6 +158,23 @@ def test_attention_decode(nh, nkv, hd, splits):
     assert ((oq.dequantize() - ref).abs() <= oq.d.repeat_interleave(32, 1) * 0.51 + 3e-3).all()
 
 
+@pytest.mark.parametrize("nb", [1, 3])
+def test_gemv_fused_argmax(nb):
+    g = torch.Generator(device=DEV).manual_seed(7 + nb)
+    N, K = 20000, 512
+    w = QWeight.random(GgmlType.Q4_K, N, K, 0.02, g, DEV)
+    x = Q8Act(nb, K, DEV)
+    ops.rmsnorm_q8(torch.randn(nb, K, device=DEV, generator=g), None, 1e-5, x, norm=False)
+    y = torch.zeros(nb, N, device=DEV)
+    slots = torch.zeros(nb, ops.ARGMAX_SLOTS, dtype=torch.int64, device=DEV)
+    ids = torch.zeros(nb, dtype=torch.int32, device=DEV)
+    for _ in range(2):  # the finalize kernel clears the slots for the next launch
+        ops.gemv(w, x, y, argmax_slots=slots)
+        ops.argmax_finalize(slots, nb, ids)
+        assert ids.tolist() == torch.argmax(y, dim=1).int().tolist()
+        assert int(slots.abs().sum()) == 0
+
+
 def test_argmax_lowest_index_on_ties():
     l = torch.randn(3, 50000, device=DEV)
     l[0, 100] = 9.0
