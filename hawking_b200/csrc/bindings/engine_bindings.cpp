@@ -4,6 +4,7 @@
 
 #include "../native/block_manager.h"
 #include "../native/scheduler.h"
+#include "../native/spec.h"
 
 namespace py = pybind11;
 using namespace hk;
@@ -64,4 +65,25 @@ void bind_engine(py::module_& m) {
       .def("prompt_len", &Scheduler::prompt_len)
       .def("state", &Scheduler::state)
       .def_property_readonly("total_preemptions", &Scheduler::total_preemptions);
+
+  py::class_<NgramDraft>(m, "NgramDraft")
+      .def(py::init<>())
+      .def("note_token", &NgramDraft::note_token)
+      .def("warm_start", &NgramDraft::warm_start)
+      .def("reset_context", &NgramDraft::reset_context)
+      .def("propose", &NgramDraft::propose, py::arg("ctx"), py::arg("k"))
+      .def_property_readonly("transitions", &NgramDraft::transitions);
+  m.def("accept_draft", [](const std::vector<int32_t>& draft, const std::vector<int32_t>& verifier) {
+    int a = 0;
+    auto out = accept_draft(draft, verifier, &a);
+    return py::make_tuple(out, a);
+  });
+  m.attr("MAX_VERIFY_BATCH") = kMaxVerifyBatch;
+  py::class_<SpecGovernor>(m, "SpecGovernor")
+      .def(py::init<int, float, int, int>(), py::arg("window") = 16, py::arg("min_accept_rate") = 0.2f,
+           py::arg("max_consecutive_rejections") = 5, py::arg("cooldown") = -1)
+      .def("step", &SpecGovernor::step)
+      .def("tick_disabled", &SpecGovernor::tick_disabled)
+      .def_property_readonly("enabled", &SpecGovernor::enabled)
+      .def_property_readonly("accept_rate", &SpecGovernor::accept_rate);
 }

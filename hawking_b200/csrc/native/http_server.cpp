@@ -12,7 +12,6 @@
 #include <algorithm>
 #include <chrono>
 #include <cstring>
-#include <sstream>
 #include <stdexcept>
 
 namespace hk {
@@ -59,13 +58,14 @@ bool write_all(int fd, const std::string& s) {
   return true;
 }
 
+// (No iostreams in this file: the module may carry its own static C++ runtime, whose stream
+// locale is not set up when no stream object is constructed at load time.)
 bool respond(int fd, int status, const std::string& ctype, const std::string& body, bool keep_alive) {
-  std::ostringstream h;
-  h << "HTTP/1.1 " << status << ' ' << status_text(status) << "\r\n"
-    << "Content-Type: " << ctype << "\r\n"
-    << "Content-Length: " << body.size() << "\r\n"
-    << "Connection: " << (keep_alive ? "keep-alive" : "close") << "\r\n\r\n";
-  return write_all(fd, h.str() + body);
+  std::string h = "HTTP/1.1 " + std::to_string(status) + " " + status_text(status) + "\r\n";
+  h += "Content-Type: " + ctype + "\r\n";
+  h += "Content-Length: " + std::to_string(body.size()) + "\r\n";
+  h += std::string("Connection: ") + (keep_alive ? "keep-alive" : "close") + "\r\n\r\n";
+  return write_all(fd, h + body);
 }
 
 std::string error_body(const std::string& message, const std::string& type, const std::string& code) {
@@ -212,15 +212,29 @@ void HttpServer::serve_connection(int fd) {
     }
     const std::string head = buf.substr(0, hend);
     buf.erase(0, hend + 4);
-    std::istringstream hs(head);
+    std::vector<std::string> lines;
+    for (size_t a = 0; a <= head.size();) {
+      size_t e = head.find("\r\n", a);
+      if (e == std::string::npos) e = head.size();
+      lines.push_back(head.substr(a, e - a));
+      a = e + 2;
+    }
     std::string method, target, version;
-    hs >> method >> target >> version;
+    {
+      const std::string& rl = lines[0];
+      const size_t s1 = rl.find(' '), s2 = s1 == std::string::npos ? s1 : rl.find(' ', s1 + 1);
+      if (s1 == std::string::npos || s2 == std::string::npos) {
+        respond_error(fd, 400, "malformed request line", "bad_request", false);
+        return;
+      }
+      method = rl.substr(0, s1);
+      target = rl.substr(s1 + 1, s2 - s1 - 1);
+      version = rl.substr(s2 + 1);
+    }
     size_t clen = 0;
     bool keep_alive = version == "HTTP/1.1";
-    std::string line;
-    std::getline(hs, line);
-    while (std::getline(hs, line)) {
-      if (!line.empty() && line.back() == '\r') line.pop_back();
+    for (size_t li = 1; li < lines.size(); ++li) {
+      const std::string& line = lines[li];
       const size_t c = line.find(':');
       if (c == std::string::npos) continue;
       const std::string k = lower(line.substr(0, c));
@@ -648,10 +662,10 @@ void HttpServer::set_metric(const std::string& name, double value, const std::st
 }
 
 std::string HttpServer::metrics_text() const {
-  std::ostringstream o;
+  std::string o;
   auto emit = [&](const std::string& name, double v, const std::string& help, bool counter) {
-    o << "# HELP " << name << ' ' << help << "\n# TYPE " << name << ' ' << (counter ? "counter" : "gauge") << '\n'
-      << name << ' ' << json_number(v) << '\n';
+    o += "# HELP " + name + " " + help + "\n# TYPE " + name + " " + (counter ? "counter" : "gauge") + "\n" + name +
+         " " + json_number(v) + "\n";
   };
   size_t queued, active;
   std::map<std::string, std::pair<double, std::pair<std::string, bool>>> extra;
@@ -669,7 +683,7 @@ std::string HttpServer::metrics_text() const {
   emit("hawking_active_slots", (double)active, "Requests being generated", false);
   emit("hawking_queued_requests", (double)queued, "Requests waiting for the engine loop", false);
   for (const auto& kv : extra) emit(kv.first, kv.second.first, kv.second.second.first, kv.second.second.second);
-  return o.str();
+  return o;
 }
 
 Json HttpServer::stats() const {

@@ -73,10 +73,24 @@ class Engine:
             free, _ = torch.cuda.mem_get_info(device)
             num_blocks = int(free * kv_fraction // bpb)
             num_blocks = min(num_blocks, max_batch * (-(-max_ctx // block_size)) + 16)
-        kv = PagedKVCache(cfg.layers, cfg.n_kv_heads, cfg.head_dim, num_blocks, block_size, max_batch,
+        # one block-table row beyond max_batch: scratch sequences (embeddings) never starve
+        kv = PagedKVCache(cfg.layers, cfg.n_kv_heads, cfg.head_dim, num_blocks, block_size, max_batch + 1,
                           -(-max_ctx // block_size), device)
         model = LlamaModel(cfg, weights, kv, max_rows=max(max_rows, max_batch), device=device)
         return Engine(cfg, model, kv, max_batch=max_batch, max_prefill_tokens=max_prefill_tokens, policy=policy)
+
+    @staticmethod
+    def from_gguf(path: str, device="cuda", max_batch: int = 8, max_ctx: Optional[int] = None, **kw):
+        """Load a GGUF model (weights re-laid for the kernels) and build an engine around it."""
+        from ..formats.gguf import GgufModel
+        from ..models.llama import load_llama_weights
+        from ..models.torch_ref import config_from_gguf
+        m = GgufModel(path)
+        cfg = config_from_gguf(m)
+        if max_ctx:
+            cfg = cfg.with_(max_ctx=max_ctx)
+        w = load_llama_weights(m, cfg, device)
+        return Engine.build(cfg, w, device=device, max_batch=max_batch, max_ctx=max_ctx, **kw)
 
     # ---- requests ----
     def add_request(self, prompt: List[int], params: Optional[SamplingParams] = None) -> int:
@@ -212,6 +226,19 @@ class Engine:
             out.append(int(m.next_ids[r].item()))
             self.stats.d2h_bytes += 4
         return out
+
+    def embed(self, ids: List[int]) -> List[float]:
+        """L2-normalised final-position logits of a teacher-forced forward of ``ids`` on a scratch
+        sequence (the reference's embedding semantics: crates/hawking-core/src/engine.rs:687-699)."""
+        sid = -next(self._ids)
+        try:
+            logits = self.model.forward_tokens(list(map(int, ids)), seq_id=sid)
+            v = logits[-1].float()
+            v = v / v.norm().clamp_min(1e-8)
+            self.stats.d2h_bytes += v.numel() * 4
+            return v.cpu().tolist()
+        finally:
+            self.kv.drop(sid)
 
     # ---- convenience ----
     def generate(self, prompts: List[List[int]], params: Optional[SamplingParams] = None) -> List[List[int]]:

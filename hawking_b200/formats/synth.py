@@ -17,6 +17,65 @@ def _gguf_arch(cfg: ModelConfig) -> str:
     return "llama" if cfg.arch in ("llama", "mixtral") else cfg.arch
 
 
+SPECIAL_TOKENS = ["<|begin_of_text|>", "<|end_of_text|>", "<|start_header_id|>", "<|end_header_id|>", "<|eot_id|>"]
+
+
+def gpt2_byte_alphabet() -> list:
+    """GPT-2 printable-byte alphabet: printable Latin-1 bytes keep their code point, the other
+    68 map to U+0100.. in byte order."""
+    keep = set(range(33, 127)) | set(range(161, 173)) | set(range(174, 256))
+    out, extra = [], 0
+    for b in range(256):
+        if b in keep:
+            out.append(chr(b))
+        else:
+            out.append(chr(256 + extra))
+            extra += 1
+    return out
+
+
+def synthetic_bpe_vocab(vocab: int):
+    """A deterministic byte-level BPE vocabulary of exactly ``vocab`` tokens: the 256 byte
+    tokens, merges over lowercase letters (space-prefixed letters, letter pairs, space-prefixed
+    pairs, letter triples, ...) and the Llama-3 control tokens at the end. Returns
+    (tokens, merges, bos_id, eos_id)."""
+    tokens = gpt2_byte_alphabet()
+    n_merge = vocab - len(tokens) - len(SPECIAL_TOKENS)
+    if n_merge < 0:
+        raise ValueError("vocab too small for a byte-level vocabulary")
+    az = [chr(c) for c in range(ord("a"), ord("z") + 1)]
+    merges = []
+
+    def gen():
+        for c in az:
+            yield ("Ġ", c)
+        for a in az:
+            for b in az:
+                yield (a, b)
+        for a in az:
+            for b in az:
+                yield ("Ġ" + a, b)
+        for a in az:
+            for b in az:
+                for c in az:
+                    yield (a + b, c)
+        for a in az:
+            for b in az:
+                for c in az:
+                    yield ("Ġ" + a + b, c)
+
+    for left, right in gen():
+        if len(merges) >= n_merge:
+            break
+        merges.append(f"{left} {right}")
+        tokens.append(left + right)
+    while len(tokens) < vocab - len(SPECIAL_TOKENS):  # pad (never produced by merges)
+        tokens.append(f"<|reserved_{len(tokens)}|>")
+    bos = len(tokens)
+    tokens += SPECIAL_TOKENS
+    return tokens, merges, bos, bos + 4
+
+
 def write_llama_family_gguf(path: str, cfg: ModelConfig, seed: int = 0, std: float = 0.02,
                             threads: int = 8) -> str:
     arch = _gguf_arch(cfg)
@@ -25,6 +84,13 @@ def write_llama_family_gguf(path: str, cfg: ModelConfig, seed: int = 0, std: flo
     et = type_id(cfg.embed_type or cfg.weight_type)
     b = GgufBuilder(arch)
     b.set("general.name", f"synthetic-{cfg.arch}")
+    toks, merges, bos, eos = synthetic_bpe_vocab(cfg.vocab)
+    b.set("tokenizer.ggml.model", "gpt2")
+    b.set("tokenizer.ggml.pre", "llama-bpe")
+    b.set("tokenizer.ggml.tokens", toks)
+    b.set("tokenizer.ggml.merges", merges)
+    b.set("tokenizer.ggml.bos_token_id", bos, 4)
+    b.set("tokenizer.ggml.eos_token_id", eos, 4)
     b.arch_set("vocab_size", cfg.vocab)
     b.arch_set("context_length", cfg.max_ctx)
     b.arch_set("embedding_length", cfg.hidden)

@@ -63,10 +63,16 @@ if os.environ.get("HK_SKIP_CUDA", "0") != "1":
     )
     cmdclass["build_ext"] = BuildExtension.with_options(use_ninja=True)
 
+# Host-only builds (HK_SKIP_CUDA=1) compile without torch's BuildExtension, whose pybind11 ABI
+# defines differ; separate object directories keep the two kinds of objects from being linked
+# into one module.
+_temp = "build/temp-host" if os.environ.get("HK_SKIP_CUDA", "0") == "1" else "build/temp-full"
+
 setup(
     name="hawking_b200",
     version="0.1.0",
     packages=["hawking_b200"],
     ext_modules=ext_modules,
     cmdclass=cmdclass,
+    options={"build_ext": {"build_temp": _temp}},
 )

@@ -1,0 +1,68 @@
+"""Serving through the real engine on the GPU: HTTP completions / chat SSE / embeddings on the tiny
+Llama-arch GGUF model (synthetic tokenizer), checked against the engine's own greedy generation."""
+import http.client
+import json
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def served(tiny_gguf, native):
+    from hawking_b200.engine.engine import Engine
+    from hawking_b200.serve import ServeLoop
+    eng = Engine.from_gguf(tiny_gguf, max_batch=4, max_ctx=256, block_size=16, num_blocks=128, max_rows=32)
+    tok = native.Tokenizer.from_gguf(native.GgufFile.open(tiny_gguf))
+    loop = ServeLoop(eng, tok, port=0, model_id="tiny").start()
+    th = loop.run_in_thread()
+    yield loop, eng, tok
+    loop.stop()
+    th.join(timeout=10)
+
+
+def post(loop, path, body):
+    c = http.client.HTTPConnection("127.0.0.1", loop.port, timeout=120)
+    c.request("POST", path, body=json.dumps(body))
+    r = c.getresponse()
+    out = r.status, r.read().decode()
+    c.close()
+    return out
+
+
+def test_completion_matches_engine_greedy(served):
+    loop, eng, tok = served
+    st, body = post(loop, "/v1/completions", {"prompt": "hello world", "max_tokens": 12, "temperature": 0})
+    assert st == 200, body
+    o = json.loads(body)
+    assert o["usage"]["completion_tokens"] <= 12
+    # the same prompt through the engine API directly (the serving loop is idle between requests)
+    from hawking_b200.engine.sampling import SamplingParams
+    ids = tok.encode("hello world")
+    loop._stop.set()
+    import time
+    time.sleep(0.2)
+    ref = eng.generate([ids], SamplingParams(max_tokens=12, stop_ids=tok.eog_ids()))[0]
+    text = tok.decode([t for t in ref if not tok.is_eog(t)])
+    assert o["choices"][0]["text"] == text
+    loop._stop.clear()
+    loop.run_in_thread()
+
+
+def test_chat_stream_and_embeddings(served):
+    loop, _, _ = served
+    c = http.client.HTTPConnection("127.0.0.1", loop.port, timeout=120)
+    c.request("POST", "/v1/chat/completions",
+              body=json.dumps({"messages": [{"role": "user", "content": "hi"}], "max_tokens": 6, "stream": True,
+                               "temperature": 0.8, "top_p": 0.9, "seed": 3}))
+    r = c.getresponse()
+    assert r.status == 200
+    raw = r.read().decode()
+    assert raw.rstrip().endswith("data: [DONE]")
+    st, body = post(loop, "/v1/embeddings", {"input": ["a b c", "hello there"]})
+    assert st == 200, body
+    vecs = [d["embedding"] for d in json.loads(body)["data"]]
+    assert len(vecs) == 2
+    for v in vecs:
+        assert abs(float(torch.tensor(v).norm()) - 1.0) < 1e-4
