@@ -240,6 +240,15 @@ class Engine:
         finally:
             self.kv.drop(sid)
 
+    def generate_speculative(self, prompt: List[int], params: Optional[SamplingParams] = None, k: int = 4):
+        """Greedy generation of one prompt with n-gram speculative decoding (bitwise the greedy
+        output). Returns (tokens, SpecStats)."""
+        from .speculative import SpeculativeDecoder
+        params = params or SamplingParams()
+        dec = SpeculativeDecoder(self, k=k)
+        out = dec.generate(prompt, params.max_tokens, params.stop_ids)
+        return out, dec.stats
+
     # ---- convenience ----
     def generate(self, prompts: List[List[int]], params: Optional[SamplingParams] = None) -> List[List[int]]:
         rids = [self.add_request(p, params) for p in prompts]

@@ -195,6 +195,7 @@ class LlamaModel:
         self.cfg, self.w, self.kv, self.dev = cfg, weights, kv, torch.device(device)
         self.max_rows = max_rows
         self.max_splits = max_splits
+        self.force_splits = 0
         H, hd, nh, nkv = cfg.hidden, cfg.head_dim, cfg.n_heads, cfg.n_kv_heads
         F = max([cfg.ffn, cfg.expert_ffn, cfg.shared_ffn, 32])
         qkv_n = (nh + 2 * nkv) * hd
@@ -233,7 +234,11 @@ class LlamaModel:
 
     def num_splits(self, rows: int) -> int:
         """KV splits per (row, kv head): the smallest power of two (at most 8, the portable
-        thread-block cluster size) that puts at least one CTA on every SM."""
+        thread-block cluster size) that puts at least one CTA on every SM. ``force_splits``
+        overrides it (speculative verify uses the single-row split so its logits are bitwise those
+        of plain greedy decode)."""
+        if self.force_splits:
+            return self.force_splits
         s = 1
         while s < min(8, self.max_splits) and rows * self.cfg.n_kv_heads * s < 148:
             s *= 2
