@@ -123,7 +123,7 @@ def main():
         barrier()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with ClockSampler(local) as cs:
+        with ClockSampler(local, period_ms=50) as cs:
             e0.record()
             for _ in range(K):
                 m.graph_forward(nseq, "greedy", advance=True)

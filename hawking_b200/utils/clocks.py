@@ -46,6 +46,15 @@ class ClockSampler:
             self.proc = subprocess.Popen(cmd, stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except FileNotFoundError:
             self.proc = None
+            return self
+        # nvidia-smi takes a while to start: wait for its first sample so that even a short timed
+        # region is covered by at least one reading taken under load.
+        import time
+        t_end = time.time() + 5.0
+        while time.time() < t_end and self.proc.poll() is None:
+            if os.path.getsize(self.path) > 0:
+                break
+            time.sleep(0.01)
         return self
 
     def __exit__(self, *exc):
