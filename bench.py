@@ -42,6 +42,8 @@ def parse():
     ap.add_argument("--ttft-runs", type=int, default=3)
     ap.add_argument("--e2e-steps", type=int, default=0, help="0 = same as --steps")
     ap.add_argument("--layers", type=int, default=0, help="override layer count (debug only; invalidates the number)")
+    ap.add_argument("--parallel", default="tp", choices=["tp", "dp"],
+                    help="N > 1: tensor parallel over the N GPUs (one model, strong scaling) or data-parallel replicas")
     ap.add_argument("--profile-step", action="store_true",
                     help="run one eager decode step between cudaProfilerStart/Stop (for ncu --profile-from-start off) "
                          "and exit without a result line")
@@ -89,12 +91,24 @@ def main():
     B, ctx, K, W = args.batch, args.ctx, args.steps, args.warmup
     max_ctx = ctx + 2 * (K + W) + 256
     cfg = cfg.with_(max_ctx=max_ctx)
+    use_tp = world > 1 and args.parallel == "tp"
     t0 = time.time()
-    w = random_llama_weights(cfg, dev, seed=0)
+    tp = None
+    if use_tp:
+        from hawking_b200.parallel.tp import TPComm, local_config, random_llama_weights_tp
+        w = random_llama_weights_tp(cfg, rank, world, dev, seed=0)
+        tp = TPComm(rank, world, 2 * cfg.layers, 8, cfg.hidden, dev)
+        mcfg = local_config(cfg, world)
+    else:
+        w = random_llama_weights(cfg, dev, seed=0)
+        mcfg = cfg
     t_load = time.time() - t0
     max_batch = max(B, 64 if args.bs64 else B)
-    eng = Engine.build(cfg, w, device=dev, max_batch=max_batch, max_ctx=max_ctx, block_size=64, max_rows=64,
-                       max_prefill_tokens=2048, kv_fraction=0.6)
+    eng = Engine.build(mcfg, w, device=dev, max_batch=max_batch, max_ctx=max_ctx, block_size=64, max_rows=64,
+                       max_prefill_tokens=2048, kv_fraction=0.6, tp=tp)
+    # aggregate over the job: data-parallel replicas each decode their own batch; a tensor-parallel
+    # group decodes one batch together
+    replicas = 1 if use_tp else world
     m, kv = eng.model, eng.kv
 
     def barrier():
@@ -163,7 +177,7 @@ def main():
     if args.bs64 and B != 64:
         seqs = setup_decode(64, 2_000_000)
         ms64, clocks64 = timed_decode(64)
-        result_bs64 = {"tok_s_aggregate": round(64 * 1000.0 / ms64 * world, 1), "ms_per_step": round(ms64, 4),
+        result_bs64 = {"tok_s_aggregate": round(64 * 1000.0 / ms64 * replicas, 1), "ms_per_step": round(ms64, 4),
                        "clocks": clocks64}
         for s in seqs:
             kv.drop(s)
@@ -200,7 +214,7 @@ def main():
                 t = torch.tensor([dt], device=dev)
                 dist.all_reduce(t, op=dist.ReduceOp.MAX)
                 dt = t.item()
-            e2e = {"value": round(n_tok * world / dt, 2), "unit": "tok/s",
+            e2e = {"value": round(n_tok * replicas / dt, 2), "unit": "tok/s",
                    "h2d_bytes_per_step": (st.h2d_bytes - h0) // max(1, KE),
                    "d2h_bytes_per_step": (st.d2h_bytes - d0) // max(1, KE),
                    "api": "Engine.step()"}
@@ -208,7 +222,7 @@ def main():
             eng.step()
     ttft_p50 = statistics.median(ttfts)
 
-    value = B * 1000.0 / ms1 * world
+    value = B * 1000.0 / ms1 * replicas
     out = {
         "metric": METRIC,
         "value": round(value, 2),
@@ -218,7 +232,7 @@ def main():
         "warmup": W,
         "ms_per_step": round(ms1, 4),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if use_tp else "weak",
         "vs_baseline": None,
         "dtype": "q4_k weights, int8 activation blocks (W4A8 dp4a), fp32 accumulate, bf16 KV",
         "data": "synthetic: random-init N(0,0.02) weights quantised to GGUF Q4_K on device; uniform-random "
@@ -226,9 +240,9 @@ def main():
         "config": {"model": "llama3-8b (Llama-3-8B-arch: 32 layers, hidden 4096, 32/8 GQA heads, head_dim 128, "
                             "FFN 14336, vocab 128256, rope theta 5e5, GGUF Q4_K)" + (
                                 f" [LAYERS OVERRIDDEN to {cfg.layers}]" if args.layers else ""),
-                   "global_batch": B * world, "seq_len": ctx,
-                   "parallelism": f"dp{world}" if world > 1 else "tp1",
-                   "l2": "inputs larger than L2: %.2f GB of weights streamed per step" % (w.nbytes / 1e9),
+                   "global_batch": B * replicas, "seq_len": ctx,
+                   "parallelism": f"tp{world}" if use_tp else (f"dp{world}" if world > 1 else "tp1"),
+                   "l2": "inputs larger than L2: %.2f GB of weights streamed per step per GPU" % (w.nbytes / 1e9),
                    "kv_block_size": 64},
         "clocks": clocks,
         "e2e": e2e,
@@ -240,9 +254,16 @@ def main():
         "weight_bw_gbs": round(w.nbytes / (ms1 * 1e-3) / 1e9, 1),
         "load_s": round(t_load, 1),
     }
+    if tp is not None:
+        tp.check()
+        out["tp_collectives"] = "decode: GEMV epilogue pushes partials over NVLink + fused all-reduce/RMSNorm; " \
+                                "prefill and bs64 (tensor-core path): NCCL all-reduce"
     if rank == 0:
         print(json.dumps(out))
     if world > 1:
+        m.release_graphs()
+        if tp is not None:
+            tp.close()
         dist.barrier()
         dist.destroy_process_group()
     return 0

@@ -1,0 +1,213 @@
+// torch bindings for the hybrid-model kernels: `.gravity` mixed-codec GEMVs (dense and routed
+// experts) and gated DeltaNet.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cuda_runtime.h>
+#include <torch/extension.h>
+
+#include <stdexcept>
+#include <string>
+
+#include "../kernels/api.h"
+#include "../kernels/kernels_api.h"
+
+namespace py = pybind11;
+using at::Tensor;
+using c10::optional;
+
+namespace {
+cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+template <typename T> T* ptr(const Tensor& t) { return reinterpret_cast<T*>(t.data_ptr()); }
+template <typename T> T* optr(const optional<Tensor>& t) { return t.has_value() ? ptr<T>(*t) : nullptr; }
+
+// Pack descriptors (codes / scales tensors + codec fields) into a device byte tensor.
+Tensor mixed_descs(const std::vector<Tensor>& codes, const std::vector<Tensor>& scales, const std::vector<int64_t>& kind,
+                   const std::vector<int64_t>& bits, const std::vector<int64_t>& group) {
+  const size_t n = codes.size();
+  TORCH_CHECK(scales.size() == n && kind.size() == n && bits.size() == n && group.size() == n, "mixed_descs: lengths");
+  std::vector<hk::MixedDesc> h(n);
+  for (size_t i = 0; i < n; ++i) {
+    TORCH_CHECK(codes[i].is_cuda() && codes[i].scalar_type() == at::kByte && codes[i].dim() == 2, "codes: uint8 [rows, bytes]");
+    TORCH_CHECK(scales[i].is_cuda() && scales[i].scalar_type() == at::kHalf && scales[i].dim() == 2, "scales: fp16 [rows, groups]");
+    TORCH_CHECK((reinterpret_cast<uintptr_t>(codes[i].data_ptr()) & 15) == 0 && codes[i].stride(0) % 16 == 0,
+                "codes rows must be 16-byte aligned");
+    h[i].codes = ptr<uint8_t>(codes[i]);
+    h[i].scales = ptr<__half>(scales[i]);
+    h[i].code_row_bytes = codes[i].stride(0);
+    h[i].scale_row_elems = scales[i].stride(0);
+    h[i].kind = (int)kind[i];
+    h[i].bits = (int)bits[i];
+    h[i].group = (int)group[i];
+    h[i].bound = kind[i] == hk::MIXED_BINARY ? 0 : (1 << (bits[i] - 1)) - 1;
+    TORCH_CHECK(kind[i] == hk::MIXED_BINARY ? bits[i] == 1 : (bits[i] == 2 || bits[i] == 4 || bits[i] == 8),
+                "mixed codec: binary (1 bit) or uniform 2/4/8 bits");
+    TORCH_CHECK(group[i] % 32 == 0, "mixed codec: group must be a multiple of 32");
+  }
+  Tensor out = torch::empty({(int64_t)(n * sizeof(hk::MixedDesc))},
+                            torch::TensorOptions().dtype(torch::kUInt8).device(codes.empty() ? torch::kCPU : codes[0].device()));
+  if (n) {
+    const c10::cuda::CUDAGuard g(codes[0].device());
+    C10_CUDA_CHECK(cudaMemcpyAsync(out.data_ptr(), h.data(), n * sizeof(hk::MixedDesc), cudaMemcpyHostToDevice,
+                                   cur_stream()));
+    C10_CUDA_CHECK(cudaStreamSynchronize(cur_stream()));
+  }
+  return out;
+}
+
+void mixed_gemv(int64_t epi, const Tensor& descs, int64_t d0, int64_t d1, int64_t N, int64_t K, const Tensor& xq,
+                const Tensor& xd, const Tensor& xs, const optional<Tensor>& y, double alpha, const optional<Tensor>& oq,
+                const optional<Tensor>& od, const optional<Tensor>& os, bool pdl, const optional<Tensor>& gate_logit) {
+  hk::MixedGemvArgs a{};
+  a.desc = reinterpret_cast<const hk::MixedDesc*>(descs.data_ptr());
+  a.d0 = (int)d0;
+  a.d1 = (int)d1;
+  a.N = (int)N;
+  a.K = (int)K;
+  a.nb = (int)xq.size(0);
+  a.xq = ptr<int8_t>(xq);
+  a.xd = ptr<float>(xd);
+  a.xs = ptr<float>(xs);
+  a.x_stride_q = xq.stride(0);
+  a.x_stride_s = xd.stride(0);
+  a.alpha = (float)alpha;
+  if (gate_logit.has_value()) {
+    a.gate_logit = ptr<float>(*gate_logit);
+    a.gate_stride = gate_logit->stride(0);
+  }
+  if (y.has_value()) {
+    a.y = ptr<float>(*y);
+    a.y_stride = y->stride(0);
+  }
+  if (oq.has_value()) {
+    a.oq = ptr<int8_t>(*oq);
+    a.od = ptr<float>(*od);
+    a.os = ptr<float>(*os);
+    a.o_stride_q = oq->stride(0);
+    a.o_stride_s = od->stride(0);
+  }
+  TORCH_CHECK(epi == hk::EPI_SWIGLU_Q8 ? a.oq != nullptr : a.y != nullptr, "mixed_gemv: output missing");
+  const c10::cuda::CUDAGuard g(xq.device());
+  hk::mixed_gemv_launch((int)epi, a, cur_stream(), pdl);
+}
+
+void moe_active(const Tensor& counts, const Tensor& active, const Tensor& n_active, bool pdl) {
+  const c10::cuda::CUDAGuard g(counts.device());
+  hk::moe_active_launch(ptr<int>(counts), (int)counts.numel(), ptr<int>(active), ptr<int>(n_active), cur_stream(), pdl);
+}
+
+void moe_mixed_gemv(int64_t epi, const Tensor& descs, int64_t base0, int64_t base1, int64_t N, int64_t K, int64_t k,
+                    const Tensor& counts, const Tensor& offsets, const Tensor& sorted, const Tensor& active,
+                    const Tensor& n_active, int64_t max_active, const Tensor& xq, const Tensor& xd, const Tensor& xs,
+                    const optional<Tensor>& oq, const optional<Tensor>& od, const optional<Tensor>& os,
+                    const optional<Tensor>& y, const optional<Tensor>& route_w, bool pdl) {
+  hk::MoeMixedArgs a{};
+  a.desc = reinterpret_cast<const hk::MixedDesc*>(descs.data_ptr());
+  a.desc_base0 = (int)base0;
+  a.desc_base1 = (int)base1;
+  a.N = (int)N;
+  a.K = (int)K;
+  a.k = (int)k;
+  a.counts = ptr<int>(counts);
+  a.offsets = ptr<int>(offsets);
+  a.sorted = ptr<int>(sorted);
+  a.active = ptr<int>(active);
+  a.n_active = ptr<int>(n_active);
+  a.xq = ptr<int8_t>(xq);
+  a.xd = ptr<float>(xd);
+  a.xs = ptr<float>(xs);
+  a.oq = optr<int8_t>(oq);
+  a.od = optr<float>(od);
+  a.os = optr<float>(os);
+  if (y.has_value()) {
+    a.y = ptr<float>(*y);
+    a.y_stride = y->stride(0);
+  }
+  a.route_w = optr<float>(route_w);
+  TORCH_CHECK(epi == 0 ? a.oq != nullptr : (a.y != nullptr && a.route_w != nullptr), "moe_mixed_gemv: outputs");
+  const c10::cuda::CUDAGuard g(xq.device());
+  hk::moe_mixed_gemv_launch((int)epi, a, (int)max_active, cur_stream(), pdl);
+}
+
+void deltanet_conv(const Tensor& qkvz, const Tensor& conv_w, const Tensor& conv_state, const optional<Tensor>& slot,
+                   int64_t kh, int64_t r, int64_t dk, int64_t dv, int64_t kc, double eps, const Tensor& q,
+                   const Tensor& k, const Tensor& v, const Tensor& z, bool pdl) {
+  hk::DeltaConvArgs a{};
+  a.qkvz = ptr<float>(qkvz);
+  a.qkvz_stride = qkvz.stride(0);
+  a.conv_w = ptr<float>(conv_w);
+  a.conv_state = ptr<float>(conv_state);
+  a.state_slot = optr<int>(slot);
+  a.kh = (int)kh;
+  a.r = (int)r;
+  a.dk = (int)dk;
+  a.dv = (int)dv;
+  a.kc = (int)kc;
+  a.eps = (float)eps;
+  a.q = ptr<float>(q);
+  a.k = ptr<float>(k);
+  a.v = ptr<float>(v);
+  a.z = ptr<float>(z);
+  const c10::cuda::CUDAGuard g(qkvz.device());
+  hk::deltanet_conv_launch(a, (int)qkvz.size(0), cur_stream(), pdl);
+}
+
+void deltanet_recurrent(const Tensor& state, const optional<Tensor>& slot, const Tensor& q, const Tensor& k,
+                        const Tensor& v, const Tensor& z, const Tensor& ba, const Tensor& a_log, const Tensor& dt_bias,
+                        int64_t r, int64_t dk, int64_t dv, const Tensor& norm_w, double eps, const optional<Tensor>& out,
+                        const Tensor& oq, const Tensor& od, const Tensor& os, bool pdl) {
+  hk::DeltaRecArgs a{};
+  a.state = ptr<float>(state);
+  a.state_slot = optr<int>(slot);
+  a.q = ptr<float>(q);
+  a.k = ptr<float>(k);
+  a.v = ptr<float>(v);
+  a.z = ptr<float>(z);
+  a.ba = ptr<float>(ba);
+  a.ba_stride = ba.stride(0);
+  a.a_log = ptr<float>(a_log);
+  a.dt_bias = ptr<float>(dt_bias);
+  a.r = (int)r;
+  a.dk = (int)dk;
+  a.dv = (int)dv;
+  a.norm_w = ptr<float>(norm_w);
+  a.eps = (float)eps;
+  a.out = optr<float>(out);
+  a.oq = ptr<int8_t>(oq);
+  a.od = ptr<float>(od);
+  a.os = ptr<float>(os);
+  const int nvh = (int)a_log.numel();
+  const c10::cuda::CUDAGuard g(q.device());
+  hk::deltanet_recurrent_launch(a, nvh, (int)q.size(0), cur_stream(), pdl);
+}
+
+void sigmoid_gate_q8(const Tensor& o, const Tensor& gate, const Tensor& oq, const Tensor& od, const Tensor& os, bool pdl) {
+  const c10::cuda::CUDAGuard g(o.device());
+  hk::sigmoid_gate_q8_launch(ptr<float>(o), ptr<float>(gate), gate.stride(0), (int)o.size(0), (int)o.size(1),
+                             ptr<int8_t>(oq), ptr<float>(od), ptr<float>(os), cur_stream(), pdl);
+}
+}  // namespace
+
+namespace hk {
+void register_model_kernels(py::module_& m) {
+  m.def("mixed_descs", &mixed_descs);
+  m.def("mixed_gemv", &mixed_gemv, py::arg("epi"), py::arg("descs"), py::arg("d0"), py::arg("d1"), py::arg("N"),
+        py::arg("K"), py::arg("xq"), py::arg("xd"), py::arg("xs"), py::arg("y") = py::none(), py::arg("alpha") = 1.0,
+        py::arg("oq") = py::none(), py::arg("od") = py::none(), py::arg("os") = py::none(), py::arg("pdl") = false,
+        py::arg("gate_logit") = py::none());
+  m.def("moe_active", &moe_active, py::arg("counts"), py::arg("active"), py::arg("n_active"), py::arg("pdl") = false);
+  m.def("moe_mixed_gemv", &moe_mixed_gemv, py::arg("epi"), py::arg("descs"), py::arg("base0"), py::arg("base1"),
+        py::arg("N"), py::arg("K"), py::arg("k"), py::arg("counts"), py::arg("offsets"), py::arg("sorted"),
+        py::arg("active"), py::arg("n_active"), py::arg("max_active"), py::arg("xq"), py::arg("xd"), py::arg("xs"),
+        py::arg("oq") = py::none(), py::arg("od") = py::none(), py::arg("os") = py::none(), py::arg("y") = py::none(),
+        py::arg("route_w") = py::none(), py::arg("pdl") = false);
+  m.def("deltanet_conv", &deltanet_conv, py::arg("qkvz"), py::arg("conv_w"), py::arg("conv_state"), py::arg("slot"),
+        py::arg("kh"), py::arg("r"), py::arg("dk"), py::arg("dv"), py::arg("kc"), py::arg("eps"), py::arg("q"),
+        py::arg("k"), py::arg("v"), py::arg("z"), py::arg("pdl") = false);
+  m.def("deltanet_recurrent", &deltanet_recurrent, py::arg("state"), py::arg("slot"), py::arg("q"), py::arg("k"),
+        py::arg("v"), py::arg("z"), py::arg("ba"), py::arg("a_log"), py::arg("dt_bias"), py::arg("r"), py::arg("dk"),
+        py::arg("dv"), py::arg("norm_w"), py::arg("eps"), py::arg("out"), py::arg("oq"), py::arg("od"), py::arg("os"),
+        py::arg("pdl") = false);
+  m.def("sigmoid_gate_q8", &sigmoid_gate_q8, py::arg("o"), py::arg("gate"), py::arg("oq"), py::arg("od"), py::arg("os"),
+        py::arg("pdl") = false);
+}
+}  // namespace hk

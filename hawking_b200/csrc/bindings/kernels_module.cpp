@@ -40,7 +40,8 @@ void gemv(int64_t fmt, int64_t epi, const std::vector<Tensor>& w0, const std::ve
           int64_t K, const optional<Tensor>& xq_, const optional<Tensor>& xd_, const optional<Tensor>& xs_,
           const optional<Tensor>& y, const optional<Tensor>& bias, const optional<Tensor>& oq,
           const optional<Tensor>& od, const optional<Tensor>& os, const optional<Tensor>& x_f32,
-          const optional<Tensor>& norm_w, double eps, bool pdl, const optional<Tensor>& argmax_slots) {
+          const optional<Tensor>& norm_w, double eps, bool pdl, const optional<Tensor>& argmax_slots,
+          int64_t argmax_offset, const optional<Tensor>& push_recv, const optional<Tensor>& push_counters) {
   hk::GemvArgs a{};
   int nb;
   if (x_f32.has_value()) {
@@ -85,6 +86,16 @@ void gemv(int64_t fmt, int64_t epi, const std::vector<Tensor>& w0, const std::ve
     TORCH_CHECK(argmax_slots->scalar_type() == at::kLong && argmax_slots->numel() >= (int64_t)nb * hk::kArgmaxSlots,
                 "gemv: argmax slots must be int64 [nb, 256]");
     a.argmax_slots = reinterpret_cast<unsigned long long*>(argmax_slots->data_ptr<int64_t>());
+    a.argmax_offset = argmax_offset;
+  }
+  if (epi == hk::EPI_PUSH) {
+    TORCH_CHECK(push_recv.has_value() && push_counters.has_value(), "gemv push: peer pointer tables required");
+    TORCH_CHECK(push_recv->is_cuda() && push_recv->scalar_type() == at::kLong && push_counters->is_cuda() &&
+                    push_counters->scalar_type() == at::kLong && push_recv->numel() == push_counters->numel(),
+                "gemv push: int64 device pointer tables of equal length");
+    a.push_recv = reinterpret_cast<float* const*>(push_recv->data_ptr<int64_t>());
+    a.push_counters = reinterpret_cast<unsigned long long* const*>(push_counters->data_ptr<int64_t>());
+    a.push_n = (int)push_recv->numel();
   }
   if (epi == hk::EPI_SWIGLU_Q8) {
     TORCH_CHECK(oq.has_value() && od.has_value() && os.has_value(), "gemv swiglu: q8 outputs required");
@@ -95,7 +106,7 @@ void gemv(int64_t fmt, int64_t epi, const std::vector<Tensor>& w0, const std::ve
     a.o_stride_q = oq->stride(0);
     a.o_stride_s = od->stride(0);
   } else {
-    TORCH_CHECK(a.y, "gemv: output y required");
+    TORCH_CHECK(a.y || epi == hk::EPI_PUSH, "gemv: output y required");
   }
   const c10::cuda::CUDAGuard g(w0[0].device());
   hk::gemv_launch((int)fmt, (int)epi, a, nb, cur_stream(), pdl);
@@ -248,7 +259,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("xq"), py::arg("xd"), py::arg("xs"), py::arg("y") = py::none(), py::arg("bias") = py::none(),
         py::arg("oq") = py::none(), py::arg("od") = py::none(), py::arg("os") = py::none(),
         py::arg("x_f32") = py::none(), py::arg("norm_w") = py::none(), py::arg("eps") = -1.0,
-        py::arg("pdl") = false, py::arg("argmax_slots") = py::none());
+        py::arg("pdl") = false, py::arg("argmax_slots") = py::none(), py::arg("argmax_offset") = 0,
+        py::arg("push_recv") = py::none(), py::arg("push_counters") = py::none());
   m.def("rmsnorm_q8", &rmsnorm_q8, py::arg("x"), py::arg("w"), py::arg("eps"), py::arg("norm"), py::arg("xq"),
         py::arg("xd"), py::arg("xs"), py::arg("y") = py::none(), py::arg("pdl") = false);
   m.def("rmsnorm", &rmsnorm, py::arg("x"), py::arg("w"), py::arg("eps"), py::arg("yf") = py::none(),
@@ -288,4 +300,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("rep_penalty"), py::arg("recent"), py::arg("uniforms"), py::arg("out"), py::arg("pdl") = false);
   m.def("embed", &embed, py::arg("fmt"), py::arg("table"), py::arg("ids"), py::arg("out"), py::arg("pdl") = false);
   hk::register_more_kernels(m);
+  hk::register_tp_kernels(m);
+  hk::register_model_kernels(m);
 }

@@ -1,0 +1,127 @@
+// torch bindings for the tensor-parallel plumbing: CUDA IPC buffers shared between the ranks of one
+// node (no multicast objects) and the fused collective kernels of tp.cu.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cuda_runtime.h>
+#include <torch/extension.h>
+
+#include <cstring>
+#include <stdexcept>
+#include <string>
+
+#include "../kernels/api.h"
+#include "../kernels/kernels_api.h"
+
+#define HK_CUDA_CHECK(expr)                                                                 \
+  do {                                                                                      \
+    cudaError_t _e = (expr);                                                                \
+    if (_e != cudaSuccess) throw std::runtime_error(std::string("CUDA error ") + cudaGetErrorString(_e)); \
+  } while (0)
+
+namespace py = pybind11;
+using at::Tensor;
+
+namespace {
+cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+template <typename T>
+T* as_ptr(int64_t p) { return reinterpret_cast<T*>(static_cast<uintptr_t>(p)); }
+
+// Device memory shareable with the other processes of this node; zero-filled.
+int64_t ipc_malloc(int64_t bytes) {
+  void* p = nullptr;
+  HK_CUDA_CHECK(cudaMalloc(&p, (size_t)bytes));
+  HK_CUDA_CHECK(cudaMemset(p, 0, (size_t)bytes));
+  return (int64_t)reinterpret_cast<uintptr_t>(p);
+}
+py::bytes ipc_handle(int64_t ptr) {
+  cudaIpcMemHandle_t h;
+  HK_CUDA_CHECK(cudaIpcGetMemHandle(&h, as_ptr<void>(ptr)));
+  return py::bytes(reinterpret_cast<const char*>(&h), sizeof h);
+}
+int64_t ipc_open(const std::string& handle) {
+  TORCH_CHECK(handle.size() == sizeof(cudaIpcMemHandle_t), "ipc_open: bad handle size");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle.data(), sizeof h);
+  void* p = nullptr;
+  HK_CUDA_CHECK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+  return (int64_t)reinterpret_cast<uintptr_t>(p);
+}
+void ipc_close(int64_t ptr) { HK_CUDA_CHECK(cudaIpcCloseMemHandle(as_ptr<void>(ptr))); }
+void ipc_free(int64_t ptr) { HK_CUDA_CHECK(cudaFree(as_ptr<void>(ptr))); }
+
+void tp_begin(const Tensor& epoch, bool pdl) {
+  TORCH_CHECK(epoch.is_cuda() && epoch.scalar_type() == at::kInt, "tp_begin: int32 CUDA epoch");
+  const c10::cuda::CUDAGuard g(epoch.device());
+  hk::tp_begin_launch(epoch.data_ptr<int>(), cur_stream(), pdl);
+}
+
+void tp_allreduce_rmsnorm_q8(const Tensor& x_in, const Tensor& x_out, int64_t recv, int64_t rank_stride, int64_t n,
+                             int64_t counter, const Tensor& epoch, int64_t producer_ctas, const c10::optional<Tensor>& w,
+                             double eps, const Tensor& xq, const Tensor& xd, const Tensor& xs, const Tensor& status,
+                             bool pdl) {
+  TORCH_CHECK(x_in.is_cuda() && x_in.scalar_type() == at::kFloat && x_out.scalar_type() == at::kFloat,
+              "tp norm: fp32 residual rows");
+  TORCH_CHECK(x_in.stride(0) == x_out.stride(0), "tp norm: x_in / x_out strides differ");
+  hk::TpReduceArgs a{};
+  a.x_in = x_in.data_ptr<float>();
+  a.x_out = x_out.data_ptr<float>();
+  a.x_stride = x_in.stride(0);
+  a.recv = as_ptr<const float>(recv);
+  a.rank_stride = rank_stride;
+  a.n = (int)n;
+  a.counter = as_ptr<const unsigned long long>(counter);
+  a.epoch = epoch.data_ptr<int>();
+  a.producer_ctas = (int)producer_ctas;
+  a.w = w.has_value() ? w->data_ptr<float>() : nullptr;
+  a.eps = (float)eps;
+  a.K = (int)x_in.size(1);
+  a.xq = xq.data_ptr<int8_t>();
+  a.xd = xd.data_ptr<float>();
+  a.xs = xs.data_ptr<float>();
+  a.status = status.data_ptr<int>();
+  const c10::cuda::CUDAGuard g(x_in.device());
+  hk::tp_allreduce_rmsnorm_q8_launch(a, (int)x_in.size(0), cur_stream(), pdl);
+}
+
+void tp_argmax(const Tensor& slots, int64_t rows, int64_t max_rows, const Tensor& keys_table, int64_t keys_local,
+               const Tensor& counters_table, int64_t counter_local, const Tensor& epoch, int64_t me, const Tensor& out,
+               const Tensor& status, bool pdl) {
+  TORCH_CHECK(slots.is_cuda() && slots.scalar_type() == at::kLong, "tp_argmax: int64 slots");
+  TORCH_CHECK(keys_table.scalar_type() == at::kLong && counters_table.scalar_type() == at::kLong &&
+                  keys_table.numel() == counters_table.numel(), "tp_argmax: int64 pointer tables");
+  hk::TpArgmaxArgs a{};
+  a.slots = reinterpret_cast<unsigned long long*>(slots.data_ptr<int64_t>());
+  a.rows = (int)rows;
+  a.max_rows = (int)max_rows;
+  a.keys = reinterpret_cast<unsigned long long* const*>(keys_table.data_ptr<int64_t>());
+  a.keys_local = as_ptr<const unsigned long long>(keys_local);
+  a.counters = reinterpret_cast<unsigned long long* const*>(counters_table.data_ptr<int64_t>());
+  a.counter_local = as_ptr<const unsigned long long>(counter_local);
+  a.uses = epoch.data_ptr<int>();
+  a.me = (int)me;
+  a.n = (int)keys_table.numel();
+  a.out = out.data_ptr<int>();
+  a.status = status.data_ptr<int>();
+  const c10::cuda::CUDAGuard g(slots.device());
+  hk::tp_argmax_launch(a, cur_stream(), pdl);
+}
+}  // namespace
+
+namespace hk {
+void register_tp_kernels(py::module_& m) {
+  m.def("ipc_malloc", &ipc_malloc, py::arg("bytes"));
+  m.def("ipc_handle", &ipc_handle, py::arg("ptr"));
+  m.def("ipc_open", &ipc_open, py::arg("handle"));
+  m.def("ipc_close", &ipc_close, py::arg("ptr"));
+  m.def("ipc_free", &ipc_free, py::arg("ptr"));
+  m.def("tp_begin", &tp_begin, py::arg("epoch"), py::arg("pdl") = false);
+  m.def("tp_allreduce_rmsnorm_q8", &tp_allreduce_rmsnorm_q8, py::arg("x_in"), py::arg("x_out"), py::arg("recv"),
+        py::arg("rank_stride"), py::arg("n"), py::arg("counter"), py::arg("epoch"), py::arg("producer_ctas"),
+        py::arg("w"), py::arg("eps"), py::arg("xq"), py::arg("xd"), py::arg("xs"), py::arg("status"),
+        py::arg("pdl") = false);
+  m.def("tp_argmax", &tp_argmax, py::arg("slots"), py::arg("rows"), py::arg("max_rows"), py::arg("keys_table"),
+        py::arg("keys_local"), py::arg("counters_table"), py::arg("counter_local"), py::arg("epoch"), py::arg("me"),
+        py::arg("out"), py::arg("status"), py::arg("pdl") = false);
+}
+}  // namespace hk

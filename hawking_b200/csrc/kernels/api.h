@@ -3,6 +3,7 @@
 // files.
 #pragma once
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -27,7 +28,7 @@ struct XQ {
 
 // ---- small-batch dequant GEMV (gemv.cu) ----
 
-enum GemvEpilogue : int { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU_Q8 = 2 };
+enum GemvEpilogue : int { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU_Q8 = 2, EPI_PUSH = 3 };
 enum GemvInput : int { XIN_Q8 = 0, XIN_NORM = 1 };
 
 struct GemvArgs {
@@ -55,8 +56,53 @@ struct GemvArgs {
   // with atomicMax, kArgmaxSlots slots per batch column (spreads the contention);
   // argmax_finalize_launch turns them into token ids and clears them for the next launch.
   unsigned long long* argmax_slots;
+  int64_t argmax_offset;   // added to row indices in the packed keys (vocabulary-parallel LM head)
+  // EPI_PUSH (tensor-parallel row-parallel projection): every output (row, column b) is stored to
+  // push_recv[p][b * N + row] on every rank p, then each CTA arrives once on push_counters[p].
+  float* const* push_recv;
+  unsigned long long* const* push_counters;
+  int push_n;
 };
 constexpr int kArgmaxSlots = 256;
+
+// ---- tensor parallel (tp.cu) ----
+struct TpSite {
+  unsigned long long* const* counters;  // [n] device pointers to every rank's counter of this site
+  int me, n;
+};
+struct TpReduceArgs {
+  const float* x_in;            // residual before the projection [rows, x_stride]
+  float* x_out;                 // residual after it (a different buffer)
+  int64_t x_stride;
+  const float* recv;            // this rank's receive region of the site: [n][rows][K] partials
+  int64_t rank_stride;          // floats between source ranks in `recv`
+  int n;
+  const unsigned long long* counter;  // this rank's arrival counter of the site
+  const int* epoch;
+  int producer_ctas;            // CTAs per rank that arrive on the counter each step
+  const float* w;               // RMSNorm weight of the next projection
+  float eps;
+  int K;
+  int8_t* xq;
+  float* xd;
+  float* xs;
+  int* status;
+};
+struct TpArgmaxArgs {
+  unsigned long long* slots;    // local fused-argmax slots [rows, kArgmaxSlots] (cleared here)
+  int rows, max_rows;
+  unsigned long long* const* keys;       // [n] device pointers: every rank's key region [n][max_rows]
+  const unsigned long long* keys_local;  // this rank's key region
+  unsigned long long* const* counters;   // [n] device pointers to every rank's counter of the site
+  const unsigned long long* counter_local;
+  int* uses;                    // this rank's count of argmax rounds (device, updated here)
+  int me, n;
+  int* out;                     // token ids [rows]
+  int* status;
+};
+void tp_begin_launch(int* epoch, cudaStream_t s, bool pdl);
+void tp_allreduce_rmsnorm_q8_launch(const TpReduceArgs& a, int rows, cudaStream_t s, bool pdl);
+void tp_argmax_launch(const TpArgmaxArgs& a, cudaStream_t s, bool pdl);
 
 void gemv_launch(int fmt, int epi, const GemvArgs& a, int nb, cudaStream_t s, bool pdl);
 
@@ -225,6 +271,94 @@ struct MoeGemvArgs {
   const float* route_w;  // [T*k]
 };
 void moe_gemv_launch(int fmt, int epi, const MoeGemvArgs& a, cudaStream_t s, bool pdl);
+
+// ---- `.gravity` mixed low-bit codecs (mixed_gemv.cu) ----
+enum MixedKind : int { MIXED_BINARY = 0, MIXED_UNIFORM = 1 };
+struct MixedDesc {            // one weight tensor [rows, K] in device memory
+  const uint8_t* codes;       // LSB-first code stream per row
+  const __half* scales;       // fp16 group scales per row
+  int64_t code_row_bytes;     // K * bits / 8
+  int64_t scale_row_elems;    // K / group
+  int kind, bits, group, bound;
+};
+struct MixedGemvArgs {
+  const MixedDesc* desc;      // device array of descriptors
+  int d0, d1;                 // descriptor indices (d1: up projection of the SwiGLU pair)
+  int N, K, nb;
+  const int8_t* xq;
+  const float* xd;
+  const float* xs;
+  int64_t x_stride_q, x_stride_s;
+  float* y;                   // STORE / RESID output [nb, y_stride]
+  int64_t y_stride;
+  float alpha;                // output scale (STORE / RESID)
+  const float* gate_logit;    // optional per-column logit g: outputs scaled by sigmoid(g) (shared-expert gate)
+  int64_t gate_stride;
+  int8_t* oq;                 // SWIGLU_Q8 output
+  float* od;
+  float* os;
+  int64_t o_stride_q, o_stride_s;
+};
+void mixed_gemv_launch(int epi, const MixedGemvArgs& a, cudaStream_t s, bool pdl);
+struct MoeMixedArgs {
+  const MixedDesc* desc;      // expert e of matrix m at desc_base_m + e
+  int desc_base0, desc_base1;
+  int N, K, k;
+  const int* counts;
+  const int* offsets;
+  const int* sorted;
+  const int* active;          // experts with pairs (moe_active), first *n_active valid
+  const int* n_active;
+  const int8_t* xq;           // sorted-order activations [T*k, K]
+  const float* xd;
+  const float* xs;
+  int8_t* oq;                 // epi 0 output (sorted order) [T*k, N]
+  float* od;
+  float* os;
+  float* y;                   // epi 1: residual rows of the tokens
+  int64_t y_stride;
+  const float* route_w;
+};
+void moe_mixed_gemv_launch(int epi, const MoeMixedArgs& a, int max_active, cudaStream_t s, bool pdl);
+void moe_active_launch(const int* counts, int E, int* active, int* n_active, cudaStream_t s, bool pdl);
+
+// ---- gated DeltaNet (deltanet.cu) ----
+struct DeltaConvArgs {
+  const float* qkvz;          // [R, qkvz_stride] fused projection (per key head: q k v z)
+  int64_t qkvz_stride;
+  const float* conv_w;        // [2*kh*dk + kh*r*dv, kc]
+  float* conv_state;          // [slots, channels, kc - 1]
+  const int* state_slot;      // [R] recurrent-state slot of each row (null: slot = row)
+  int kh, r, dk, dv, kc;
+  float eps;
+  float* q;                   // [R, kh*r, dk] (L2-normalised, scaled)
+  float* k;                   // [R, kh*r, dk]
+  float* v;                   // [R, kh*r*dv]
+  float* z;                   // [R, kh*r*dv]
+};
+void deltanet_conv_launch(const DeltaConvArgs& a, int rows, cudaStream_t s, bool pdl);
+struct DeltaRecArgs {
+  float* state;               // [slots, kh*r, dk, dv]
+  const int* state_slot;
+  const float* q;
+  const float* k;
+  const float* v;
+  const float* z;
+  const float* ba;            // [R, ba_stride] (per key head: b[r] a[r])
+  int64_t ba_stride;
+  const float* a_log;         // [kh*r]
+  const float* dt_bias;       // [kh*r]
+  int r, dk, dv;
+  const float* norm_w;        // [dv]
+  float eps;
+  float* out;                 // optional fp32 [R, kh*r*dv]
+  int8_t* oq;                 // q8 [R, kh*r*dv]
+  float* od;
+  float* os;
+};
+void deltanet_recurrent_launch(const DeltaRecArgs& a, int n_value_heads, int rows, cudaStream_t s, bool pdl);
+void sigmoid_gate_q8_launch(const float* o, const float* gate, int64_t gate_stride, int rows, int W, int8_t* oq,
+                            float* od, float* os, cudaStream_t s, bool pdl);
 
 // ---- quantisers (quantize.cu) ----
 // n elements (rows * cols, cols a multiple of the block) -> planes p0..p3 of format fmt.

@@ -15,6 +15,7 @@
 // gemm_q4_k_m_fused*, _pair* gate+up with SwiGLU, _add residual-fused variants, add_rmsnorm_fused_q8
 // feeding them); numerics oracle crates/hawking-core/src/quant.rs:722 (gemv_q4_k_q8k).
 #include "gemv.cuh"
+#include "tp.cuh"
 
 #include <cooperative_groups.h>
 
@@ -268,6 +269,24 @@ __global__ void __launch_bounds__(256, (NB == 1 && XIN == XIN_Q8) ? (EPI == EPI_
       }
     }
     cluster.sync();  // the other CTAs' shared memory stays alive until the first CTA has read it
+  } else if constexpr (EPI == EPI_PUSH) {
+    // tensor parallel: partial rows to every rank's receive region, then one arrival per CTA
+    float acc[NB];
+    if (live) {
+      row_dot<FMT, NB>(a.w0, row, n_units, wg, x, nb, acc);
+#pragma unroll
+      for (int b = 0; b < NB; ++b) acc[b] = warp_sum(acc[b]);
+    }
+    pdl_launch();
+    if (live && lane < nb) {
+      float v = acc[0];
+#pragma unroll
+      for (int c = 1; c < NB; ++c)
+        if (lane == c) v = acc[c];
+      if (a.bias) v += a.bias[row];
+      for (int p = 0; p < a.push_n; ++p) a.push_recv[p][(int64_t)lane * a.N + row] = v;
+    }
+    tp_signal(TpSite{a.push_counters, 0, a.push_n});
   } else {
     if (!live) { pdl_launch(); return; }
     float acc[NB];
@@ -286,7 +305,8 @@ __global__ void __launch_bounds__(256, (NB == 1 && XIN == XIN_Q8) ? (EPI == EPI_
       else *y = v;
       if constexpr (EPI == EPI_STORE) {
         if (a.argmax_slots)
-          atomicMax(a.argmax_slots + (int64_t)lane * kArgmaxSlots + (row % kArgmaxSlots), argmax_key(v, (int)row));
+          atomicMax(a.argmax_slots + (int64_t)lane * kArgmaxSlots + (row % kArgmaxSlots),
+                    argmax_key(v, (int)(row + a.argmax_offset)));
       }
     }
   }
@@ -323,7 +343,8 @@ static void dispatch_fmt(int fmt, const GemvArgs& a, int nb, cudaStream_t s, boo
 }
 
 void gemv_launch(int fmt, int epi, const GemvArgs& a, int nb, cudaStream_t s, bool pdl) {
-  if (a.K % 128) throw std::runtime_error("gemv: K must be a multiple of 128");
+  // whole weight units: 32-element chunks (Q4_0 / Q8_0), 128-element units (Q5_0), 256 (K-quants)
+  if (a.K % 32 || ((fmt == WF_Q5_0) && a.K % 128)) throw std::runtime_error("gemv: K must be a multiple of the weight unit");
   if ((fmt == WF_Q4_K || fmt == WF_Q6_K) && a.K % 256) throw std::runtime_error("gemv: K-quant rows need K % 256 == 0");
   if (a.K > 65536) throw std::runtime_error("gemv: K too large for the shared activation buffer");
   if (epi == EPI_SWIGLU_Q8 && a.N % 32) throw std::runtime_error("gemv swiglu: N must be a multiple of 32");
@@ -337,6 +358,10 @@ void gemv_launch(int fmt, int epi, const GemvArgs& a, int nb, cudaStream_t s, bo
   switch (epi) {
     case EPI_STORE: dispatch_fmt<EPI_STORE, XIN_Q8>(fmt, a, nb, s, pdl); break;
     case EPI_RESID: dispatch_fmt<EPI_RESID, XIN_Q8>(fmt, a, nb, s, pdl); break;
+    case EPI_PUSH:
+      if (!a.push_recv || !a.push_counters || a.push_n <= 0) throw std::runtime_error("gemv push: peer tables required");
+      dispatch_fmt<EPI_PUSH, XIN_Q8>(fmt, a, nb, s, pdl);
+      break;
     case EPI_SWIGLU_Q8: dispatch_fmt<EPI_SWIGLU_Q8, XIN_Q8>(fmt, a, nb, s, pdl); break;
     default: throw std::runtime_error("gemv: bad epilogue");
   }

@@ -1,0 +1,240 @@
+// `.gravity` sub-2-bit / low-bit GEMV (K8): binary sign + group scale (HGRAVB01) and uniform
+// 2/4/8-bit group codes (HGRAVU01; 2-bit with bound 1 is the ternary point), dequantised in
+// registers against q8 activation blocks with dp4a.
+//
+// Storage on the GPU is the codec's own payload bytes, split into two planes per tensor: the
+// LSB-first code stream of every row ([rows, K * bits / 8] bytes, exactly the body bits) and the
+// fp16 group scales ([rows, K / group]). A per-tensor descriptor carries the codec, so one launch
+// can mix codecs across experts (the per-tensor bit assignment of a mixed artifact).
+//
+// Per 32-element activation block (d_x, s_x = d_x * sum q):
+//   binary   w_i = s_g * (2 b_i - 1):        s_g * (2 d_x sum_{b_i=1} q_i - s_x)
+//   uniform  w_i = s_g * (c_i - bound):      s_g * (d_x sum c_i q_i - bound * s_x)
+// Bits are widened to bytes with shift-multiply (1 bit) or shift-OR (2 bits) spreads, or nibble masks with a
+// byte permute of the activations (4 bits, LSB-first pairs), then one dp4a per 4 elements.
+//
+// Dense kernel: one warp per output row, lane = 32-element blocks lane, lane + 32, ...;
+// epilogues STORE (fp32), RESID (+=) and SWIGLU_Q8 (gate/up descriptor pair -> q8, 32 rows per
+// CTA). Expert kernel: the routed (token, expert) pairs in expert order (moe_align), one grid row
+// per active expert, chunks of <= 8 pairs; SwiGLU -> q8 in pair order, or the route-weighted
+// atomic add into each token's residual.
+//
+// Parity: crates/hawking-core/src/model/qwen_complete_binary/q80_mixed_decode.rs:135-1070
+// (binary / uniform matvec oracles), crates/hawking-core/shaders/q80_mixed_decode.metal and
+// qwen_uniform_q4.metal / qwen_binary*.metal (packed matvec families),
+// qwen80_all_ten_routed_expert_wave.metal (10 routed experts through a 512-way expert table).
+#include "api.h"
+#include "qformats.cuh"
+
+namespace hk {
+
+// 4 bits -> 4 bytes of 0/1 (bit k to byte k).
+__device__ __forceinline__ uint32_t spread1(uint32_t nib) { return (nib * 0x00204081u) & 0x01010101u; }
+// 4 two-bit codes (one byte) -> 4 bytes (shifted copies overlap, so OR them: no carries).
+__device__ __forceinline__ uint32_t spread2(uint32_t byte) {
+  return (byte | (byte << 6) | (byte << 12) | (byte << 18)) & 0x03030303u;
+}
+
+// Dot of one 32-element block of row `row` of tensor `t` with activation block `blk`.
+__device__ __forceinline__ float mixed_block_dot(const MixedDesc& t, int64_t row, int blk, const int8_t* xq,
+                                                  float dx, float sx) {
+  const uint8_t* codes = t.codes + row * t.code_row_bytes;
+  const float sg = __half2float(t.scales[row * t.scale_row_elems + (blk * 32) / t.group]);
+  const int4 qa = *reinterpret_cast<const int4*>(xq + blk * 32);
+  const int4 qb = *reinterpret_cast<const int4*>(xq + blk * 32 + 16);
+  const int q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+  int dot = 0;
+  if (t.kind == MIXED_BINARY) {
+    const uint32_t b = __ldg(reinterpret_cast<const uint32_t*>(codes) + blk);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) dot = dp4a((int)spread1((b >> (4 * j)) & 0xFu), q[j], dot);
+    return sg * (2.f * dx * (float)dot - sx);
+  }
+  if (t.bits == 2) {
+    const uint2 w = __ldg(reinterpret_cast<const uint2*>(codes) + blk);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) dot = dp4a((int)spread2((w.x >> (8 * j)) & 0xFFu), q[j], dot);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) dot = dp4a((int)spread2((w.y >> (8 * j)) & 0xFFu), q[4 + j], dot);
+  } else if (t.bits == 4) {
+    const uint4 w = __ldg(reinterpret_cast<const uint4*>(codes) + blk);
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {  // word j: elements 8j..8j+7, element 8j+2i in the low nibble of byte i
+      const int even = (int)__byte_perm((uint32_t)q[2 * j], (uint32_t)q[2 * j + 1], 0x6420);
+      const int odd = (int)__byte_perm((uint32_t)q[2 * j], (uint32_t)q[2 * j + 1], 0x7531);
+      dot = dp4a((int)(ws[j] & 0x0F0F0F0Fu), even, dot);
+      dot = dp4a((int)((ws[j] >> 4) & 0x0F0F0F0Fu), odd, dot);
+    }
+  } else {  // 8 bits: codes c as signed (c - 128), so sum (c - bound) q = dot + (128 - bound) sum q
+    const uint4 w0 = __ldg(reinterpret_cast<const uint4*>(codes) + 2 * blk);
+    const uint4 w1 = __ldg(reinterpret_cast<const uint4*>(codes) + 2 * blk + 1);
+    const uint32_t ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) dot = dp4a((int)(ws[j] ^ 0x80808080u), q[j], dot);
+    return sg * (dx * (float)dot + (float)(128 - t.bound) * sx);
+  }
+  return sg * (dx * (float)dot - (float)t.bound * sx);
+}
+
+__device__ __forceinline__ float mixed_row_dot(const MixedDesc& t, int64_t row, int K, const int8_t* xq,
+                                               const float* xd, const float* xs) {
+  const int lane = threadIdx.x & 31;
+  float acc = 0.f;
+  for (int blk = lane; blk < K / 32; blk += 32) acc += mixed_block_dot(t, row, blk, xq, xd[blk], xs[blk]);
+  return warp_sum(acc);
+}
+
+// ---- dense ------------------------------------------------------------------------------------
+template <int EPI>
+__global__ void __launch_bounds__(256) mixed_gemv_kernel(MixedGemvArgs a) {
+  __shared__ float hbuf[8][32];
+  pdl_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const MixedDesc t0 = a.desc[a.d0];
+  for (int b = 0; b < a.nb; ++b) {
+    const int8_t* xq = a.xq + (int64_t)b * a.x_stride_q;
+    const float* xd = a.xd + (int64_t)b * a.x_stride_s;
+    const float* xs = a.xs + (int64_t)b * a.x_stride_s;
+    if constexpr (EPI == EPI_SWIGLU_Q8) {
+      const MixedDesc t1 = a.desc[a.d1];
+#pragma unroll 1
+      for (int r = 0; r < 4; ++r) {
+        const int n = blockIdx.x * 32 + warp * 4 + r;
+        float h = 0.f;
+        if (n < a.N) {
+          const float g = mixed_row_dot(t0, n, a.K, xq, xd, xs);
+          const float u = mixed_row_dot(t1, n, a.K, xq, xd, xs);
+          h = g / (1.f + __expf(-g)) * u;
+        }
+        if (lane == 0) hbuf[warp][r] = h;
+      }
+      __syncthreads();
+      if (warp == 0) {
+        const int n = blockIdx.x * 32 + lane;
+        const float v = hbuf[lane >> 2][lane & 3];
+        const float amax = warp_max(fabsf(v));
+        const float d = amax / 127.f;
+        const int q = amax > 0.f ? __float2int_rn(v / d) : 0;
+        const float qs = warp_sum((float)q);
+        if (n < a.N) a.oq[(int64_t)b * a.o_stride_q + n] = (int8_t)q;
+        if (lane == 0 && n < a.N) {
+          a.od[(int64_t)b * a.o_stride_s + (n >> 5)] = d;
+          a.os[(int64_t)b * a.o_stride_s + (n >> 5)] = d * qs;
+        }
+      }
+      __syncthreads();
+    } else {
+      const int n = blockIdx.x * 8 + warp;
+      if (n < a.N) {
+        float v = mixed_row_dot(t0, n, a.K, xq, xd, xs) * a.alpha;
+        if (a.gate_logit) v *= 1.f / (1.f + __expf(-a.gate_logit[(int64_t)b * a.gate_stride]));
+        if (lane == 0) {
+          float* y = a.y + (int64_t)b * a.y_stride + n;
+          if constexpr (EPI == EPI_RESID) *y += v;
+          else *y = v;
+        }
+      }
+    }
+  }
+  pdl_launch();
+}
+
+void mixed_gemv_launch(int epi, const MixedGemvArgs& a, cudaStream_t s, bool pdl) {
+  if (a.K % 32) throw std::runtime_error("mixed gemv: K must be a multiple of 32");
+  if (epi == EPI_SWIGLU_Q8) {
+    if (a.N % 32) throw std::runtime_error("mixed gemv swiglu: N must be a multiple of 32");
+    launch(mixed_gemv_kernel<EPI_SWIGLU_Q8>, dim3(a.N / 32), dim3(256), 0, s, pdl, a);
+  } else if (epi == EPI_RESID) {
+    launch(mixed_gemv_kernel<EPI_RESID>, dim3((a.N + 7) / 8), dim3(256), 0, s, pdl, a);
+  } else {
+    launch(mixed_gemv_kernel<EPI_STORE>, dim3((a.N + 7) / 8), dim3(256), 0, s, pdl, a);
+  }
+}
+
+// ---- routed experts ----------------------------------------------------------------------------
+// Grid (row blocks, active experts): blockIdx.y indexes a.active (experts with >= 1 pair).
+template <int EPI>
+__global__ void __launch_bounds__(256) moe_mixed_gemv_kernel(MoeMixedArgs a) {
+  __shared__ float hbuf[8][8][4];
+  pdl_wait();
+  const int na = *a.n_active;
+  if ((int)blockIdx.y >= na) { pdl_launch(); return; }
+  const int e = a.active[blockIdx.y];
+  const int c = a.counts[e], off = a.offsets[e];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const MixedDesc tg = a.desc[a.desc_base0 + e];
+  const MixedDesc tu = EPI == 0 ? a.desc[a.desc_base1 + e] : tg;
+  for (int p = 0; p < c; ++p) {
+    const int sp = off + p;  // sorted pair index
+    const int8_t* xq = a.xq + (int64_t)sp * a.K;
+    const float* xd = a.xd + (int64_t)sp * (a.K / 32);
+    const float* xs = a.xs + (int64_t)sp * (a.K / 32);
+    if constexpr (EPI == 0) {
+#pragma unroll 1
+      for (int r = 0; r < 4; ++r) {
+        const int n = blockIdx.x * 32 + warp * 4 + r;
+        const float g = mixed_row_dot(tg, n, a.K, xq, xd, xs);
+        const float u = mixed_row_dot(tu, n, a.K, xq, xd, xs);
+        if (lane == 0) hbuf[warp][r][0] = g / (1.f + __expf(-g)) * u;
+      }
+      __syncthreads();
+      if (warp == 0) {
+        const int n = blockIdx.x * 32 + lane;
+        const float v = hbuf[lane >> 2][lane & 3][0];
+        const float amax = warp_max(fabsf(v));
+        const float d = amax / 127.f;
+        const int q = amax > 0.f ? __float2int_rn(v / d) : 0;
+        const float qs = warp_sum((float)q);
+        a.oq[(int64_t)sp * a.N + n] = (int8_t)q;
+        if (lane == 0) {
+          a.od[(int64_t)sp * (a.N / 32) + (n >> 5)] = d;
+          a.os[(int64_t)sp * (a.N / 32) + (n >> 5)] = d * qs;
+        }
+      }
+      __syncthreads();
+    } else {
+      const int n = blockIdx.x * 8 + warp;
+      const float v = mixed_row_dot(tg, n, a.K, xq, xd, xs);
+      if (lane == 0) {
+        const int pair = a.sorted[sp];
+        atomicAdd(a.y + (int64_t)(pair / a.k) * a.y_stride + n, a.route_w[pair] * v);
+      }
+    }
+  }
+  pdl_launch();
+}
+
+void moe_mixed_gemv_launch(int epi, const MoeMixedArgs& a, int max_active, cudaStream_t s, bool pdl) {
+  if (a.K % 32) throw std::runtime_error("moe mixed gemv: K must be a multiple of 32");
+  if (epi == 0) {
+    if (a.N % 32) throw std::runtime_error("moe mixed gemv: expert FFN width must be a multiple of 32");
+    launch(moe_mixed_gemv_kernel<0>, dim3(a.N / 32, max_active), dim3(256), 0, s, pdl, a);
+  } else {
+    if (a.N % 8) throw std::runtime_error("moe mixed gemv: hidden must be a multiple of 8");
+    launch(moe_mixed_gemv_kernel<1>, dim3(a.N / 8, max_active), dim3(256), 0, s, pdl, a);
+  }
+}
+
+// Compact list of experts with at least one routed pair (for the expert grid's y dimension).
+__global__ void moe_active_kernel(const int* counts, int E, int* active, int* n_active) {
+  pdl_wait();
+  __shared__ int n;
+  if (threadIdx.x == 0) n = 0;
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    if (counts[e] > 0) {
+      const int slot = atomicAdd(&n, 1);
+      active[slot] = e;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *n_active = n;
+  pdl_launch();
+}
+
+void moe_active_launch(const int* counts, int E, int* active, int* n_active, cudaStream_t s, bool pdl) {
+  launch(moe_active_kernel, dim3(1), dim3(512), 0, s, pdl, counts, E, active, n_active);
+}
+
+}  // namespace hk

@@ -65,7 +65,8 @@ class Engine:
     @staticmethod
     def build(cfg: ModelConfig, weights, device="cuda", max_batch: int = 8, max_ctx: Optional[int] = None,
               block_size: int = 64, num_blocks: Optional[int] = None, max_rows: int = 64,
-              max_prefill_tokens: int = 512, kv_fraction: float = 0.5, policy: int = 0):
+              max_prefill_tokens: int = 512, kv_fraction: float = 0.5, policy: int = 0, tp=None):
+        """``tp`` (parallel.tp.TPComm): ``cfg`` and ``weights`` are this rank's tensor-parallel shard."""
         from ..models.llama import LlamaModel
         max_ctx = max_ctx or cfg.max_ctx
         bpb = PagedKVCache.bytes_per_block(cfg.layers, cfg.n_kv_heads, cfg.head_dim, block_size)
@@ -76,7 +77,7 @@ class Engine:
         # one block-table row beyond max_batch: scratch sequences (embeddings) never starve
         kv = PagedKVCache(cfg.layers, cfg.n_kv_heads, cfg.head_dim, num_blocks, block_size, max_batch + 1,
                           -(-max_ctx // block_size), device)
-        model = LlamaModel(cfg, weights, kv, max_rows=max(max_rows, max_batch), device=device)
+        model = LlamaModel(cfg, weights, kv, max_rows=max(max_rows, max_batch), device=device, tp=tp)
         return Engine(cfg, model, kv, max_batch=max_batch, max_prefill_tokens=max_prefill_tokens, policy=policy)
 
     @staticmethod

@@ -191,8 +191,11 @@ class LlamaModel:
     """Runs the forward over static buffers for up to ``max_rows`` rows."""
 
     def __init__(self, cfg: ModelConfig, weights: LlamaWeights, kv, max_rows: int = 8, device="cuda",
-                 max_splits: int = 64):
+                 max_splits: int = 64, tp=None):
+        """``cfg`` describes this rank's shard when ``tp`` (parallel.tp.TPComm) is given: heads and
+        FFN width already divided by the tensor-parallel degree."""
         self.cfg, self.w, self.kv, self.dev = cfg, weights, kv, torch.device(device)
+        self.tp = tp
         self.max_rows = max_rows
         self.max_splits = max_splits
         self.force_splits = 0
@@ -211,7 +214,10 @@ class LlamaModel:
         self.part_o = torch.zeros(cap * nh * hd, device=self.dev)
         self.part_lse = torch.zeros(cap * nh, device=self.dev)
         self.attn_counters = torch.zeros(R * nkv, dtype=torch.int32, device=self.dev)
-        self.logits = torch.zeros(R, cfg.vocab, device=self.dev)
+        self.logits = torch.zeros(R, weights.lm_head.N, device=self.dev)
+        if tp is not None:
+            self.x2 = torch.zeros(R, H, device=self.dev)       # second residual buffer (push all-reduce)
+            self.partial = torch.zeros(R, H, device=self.dev)  # prefill partial sums (NCCL all-reduce)
         # tensor-core path buffers (bf16 activations; fp32 outputs kept zeroed between uses)
         self.xb = torch.zeros(R, H, dtype=torch.bfloat16, device=self.dev)
         self.attb = torch.zeros(R, nh * hd, dtype=torch.bfloat16, device=self.dev)
@@ -266,9 +272,15 @@ class LlamaModel:
         inp = self.inp
         x = self.x[:rows]
         tc = self.use_tensor_cores(rows)
+        tp = self.tp
+        if tp is not None and not tc:
+            ops.tp_begin(tp)  # one epoch per forward that uses the push all-reduce sites
         ops.embed(w.embed, inp.ids[:rows], x)
         splits = self.num_splits(rows)
         for l, lw in enumerate(w.layers):
+            if tp is not None and not tc:
+                self._layer_gemv_tp(l, lw, rows, splits)
+                continue
             if tc:
                 self._attention_block_tc(l, lw, rows, splits)
                 self._ffn_block_tc(lw, rows)
@@ -289,6 +301,11 @@ class LlamaModel:
                 ops.advance(inp.ids, self.next_ids, inp.positions, inp.row_ctx, rows)
             return
         nl = n_logits or rows
+        if tp is not None:
+            self._lm_head_tp(rows, nl, n_logits, tc, sample)
+            if advance:
+                ops.advance(inp.ids, self.next_ids, inp.positions, inp.row_ctx, rows)
+            return
         if tc and w.lm_head.fmt == GgmlType.Q4_K:
             ops.rmsnorm(x, w.out_norm, cfg.eps, yb=self.xb[:rows])
             src = self.xb[:rows]
@@ -344,6 +361,59 @@ class LlamaModel:
         self._gemv_cols(lambda c0, c1: ops.gemv(lw.wo, self._q8_slice(self.att, c0, c1), x[c0:c1],
                                                 residual=True), rows)
 
+    # ---- tensor parallel (decode GEMV path: fused push all-reduce; see parallel/tp.py) ----
+    def _layer_gemv_tp(self, l, lw, rows, splits):
+        cfg, w, tp = self.cfg, self.w, self.tp
+        if rows > GEMV_COLS:
+            raise RuntimeError("tensor-parallel GEMV path takes at most 8 rows")
+        xa_res, xb_res = self.x[:rows], self.x2[:rows]
+        if l == 0:
+            ops.rmsnorm_q8(xa_res, lw.attn_norm, cfg.eps, self.xa.view(rows))
+        # (for l > 0 the previous layer's FFN all-reduce already left norm(x) in self.xa)
+        xa = self.xa_view(0, rows)
+        off = 0
+        for wt in lw.wqkv:
+            ops.gemv(wt, xa, self.qkv[:rows, off:off + wt.N])
+            off += wt.N
+        self._rope_attention(l, lw, rows, splits, out_q8=self.att.view(rows))
+        ops.gemv_push(lw.wo, self._q8_slice(self.att, 0, rows), tp, 2 * l)
+        ops.tp_allreduce_rmsnorm_q8(tp, 2 * l, xa_res, xb_res, lw.ffn_norm, cfg.eps, self.xa.view(rows),
+                                    producer_ctas=-(-lw.wo.N // 8))
+        ops.gemv_swiglu(lw.w_gate, lw.w_up, self.xa_view(0, rows), self._q8_slice(self.hq, 0, rows))
+        ops.gemv_push(lw.w_down, self._q8_slice(self.hq, 0, rows, lw.w_down.K), tp, 2 * l + 1)
+        nxt = w.layers[l + 1].attn_norm if l + 1 < len(w.layers) else w.out_norm
+        ops.tp_allreduce_rmsnorm_q8(tp, 2 * l + 1, xb_res, xa_res, nxt, cfg.eps, self.xa.view(rows),
+                                    producer_ctas=-(-lw.w_down.N // 8))
+
+    def _allreduce_partial_tc(self, rows):
+        """Prefill (tensor-core path): NCCL all-reduce of this rank's partial, added to x."""
+        import torch.distributed as dist
+        p = self.partial[:rows]
+        dist.all_reduce(p, group=self.tp.group)
+        self.x[:rows].add_(p)
+
+    def _lm_head_tp(self, rows, nl, n_logits, tc, sample):
+        w, cfg, tp = self.w, self.cfg, self.tp
+        if sample not in ("greedy", "none"):
+            raise NotImplementedError("tensor-parallel sampling: greedy only")
+        if n_logits < 0:
+            return
+        if nl > GEMV_COLS:
+            raise RuntimeError("tensor-parallel LM head takes at most 8 rows")
+        if tc or n_logits:
+            # the residual is in self.x; normalise the sampled rows here
+            src = self.x[:rows]
+            if n_logits:
+                src = self.x.index_select(0, self.logit_rows[:nl].long())
+            ops.rmsnorm_q8(src, w.out_norm, cfg.eps, self.xa.view(nl))
+        # else: the last layer's all-reduce left norm(x) in self.xa
+        if sample == "none":  # this rank's vocabulary slice of the logits only
+            ops.gemv(w.lm_head, self.xa_view(0, nl), self.logits[:nl])
+            return
+        ops.gemv(w.lm_head, self.xa_view(0, nl), self.logits[:nl], argmax_slots=self.argmax_slots[:nl],
+                 argmax_offset=tp.rank * w.lm_head.N)
+        ops.tp_argmax(tp, self.argmax_slots, nl, self.next_ids)
+
     def _attention_block_tc(self, l, lw, rows, splits):
         x = self.x[:rows]
         ops.rmsnorm(x, lw.attn_norm, self.cfg.eps, yb=self.xb[:rows])
@@ -354,7 +424,12 @@ class LlamaModel:
             ops.tc_gemm(wt, self.xb[:rows], qkv[:, off:off + wt.N], self.status, y_zeroed=True)
             off += wt.N
         self._rope_attention(l, lw, rows, splits, out_bf16=self.attb[:rows])
-        ops.tc_gemm(lw.wo, self.attb[:rows], x, self.status, atomic=True)
+        if self.tp is not None:
+            self.partial[:rows].zero_()
+            ops.tc_gemm(lw.wo, self.attb[:rows], self.partial[:rows], self.status, atomic=True, y_zeroed=True)
+            self._allreduce_partial_tc(rows)
+        else:
+            ops.tc_gemm(lw.wo, self.attb[:rows], x, self.status, atomic=True)
 
     def _ffn_block_tc(self, lw, rows):
         x = self.x[:rows]
@@ -363,7 +438,12 @@ class LlamaModel:
         gu = self.gu[:rows, : 2 * F]
         ops.tc_gemm(lw.w_gu, self.xb[:rows], gu, self.status, y_zeroed=True)
         ops.swiglu_bf16(gu, F, self.hb[:rows, :F], clear=True)
-        ops.tc_gemm(lw.w_down, self.hb[:rows, :F], x, self.status, atomic=True)
+        if self.tp is not None:
+            self.partial[:rows].zero_()
+            ops.tc_gemm(lw.w_down, self.hb[:rows, :F], self.partial[:rows], self.status, atomic=True, y_zeroed=True)
+            self._allreduce_partial_tc(rows)
+        else:
+            ops.tc_gemm(lw.w_down, self.hb[:rows, :F], x, self.status, atomic=True)
 
     def forward_tokens(self, tokens, seq_id: int = -1, start_pos: int = 0) -> torch.Tensor:
         """Teacher-forced forward of ``tokens`` for one sequence (positions start_pos..), returning
@@ -374,7 +454,7 @@ class LlamaModel:
             raise RuntimeError("KV pool exhausted")
         kv.sync_tables([seq_id])
         r = kv.row(seq_id)
-        out = torch.empty(n, self.cfg.vocab, device=self.dev)
+        out = torch.empty(n, self.logits.shape[1], device=self.dev)  # this rank's vocabulary slice under TP
         for c0 in range(0, n, self.max_rows):
             c1 = min(n, c0 + self.max_rows)
             pos = list(range(start_pos + c0, start_pos + c1))
@@ -396,6 +476,12 @@ class LlamaModel:
 
     # ---- CUDA graphs ----
     def graph_forward(self, rows: int, sample: str = "greedy", advance: bool = False):
+        if self.tp is not None and self.use_tensor_cores(rows):
+            # the tensor-core path all-reduces with NCCL: run it eagerly rather than capture NCCL
+            n0 = ops.launches.n
+            self.forward(rows, sample, advance)
+            self.launches_per_graph = ops.launches.n - n0
+            return
         key = (rows, sample, advance)
         g = self._graphs.get(key)
         if g is None:

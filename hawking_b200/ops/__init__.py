@@ -60,15 +60,48 @@ def rmsnorm(x, w, eps, yf=None, yb=None):
     kernels().rmsnorm(x, w, eps, yf, yb, PDL)
 
 
-def gemv(w: QWeight, x: Q8Act, y: torch.Tensor, residual: bool = False, bias=None, argmax_slots=None):
+def gemv(w: QWeight, x: Q8Act, y: torch.Tensor, residual: bool = False, bias=None, argmax_slots=None,
+         argmax_offset: int = 0):
     """y[b] = W x[b] (or y += ... with ``residual``). ``argmax_slots`` (int64 [nb, 256], zeroed)
-    additionally folds every output into packed greedy keys; ``argmax_finalize`` reads them."""
+    additionally folds every output into packed greedy keys (row index + ``argmax_offset``);
+    ``argmax_finalize`` reads them."""
     launches.add()
     kernels().gemv(w.fmt, EPI_RESID if residual else EPI_STORE, w.planes, [], w.N, w.K, x.q, x.d, x.s, y, bias,
-                   None, None, None, None, None, -1.0, PDL, argmax_slots)
+                   None, None, None, None, None, -1.0, PDL, argmax_slots, argmax_offset)
 
 
 ARGMAX_SLOTS = 256
+EPI_PUSH = 3
+
+
+def gemv_push(w: QWeight, x: Q8Act, tp, site: int, bias=None):
+    """Row-parallel projection: the partial outputs go to every rank's receive region of ``site``
+    (tensor-parallel all-reduce push, see parallel/tp.py)."""
+    launches.add()
+    kernels().gemv(w.fmt, EPI_PUSH, w.planes, [], w.N, w.K, x.q, x.d, x.s, None, bias, None, None, None, None, None,
+                   -1.0, PDL, None, 0, tp.push_recv[site], tp.push_counters[site])
+
+
+def tp_begin(tp):
+    launches.add()
+    kernels().tp_begin(tp.epoch, PDL)
+
+
+def tp_allreduce_rmsnorm_q8(tp, site: int, x_in: torch.Tensor, x_out: torch.Tensor, w, eps: float, out: Q8Act,
+                            producer_ctas: int):
+    """x_out = x_in + sum of every rank's partials at ``site``; then RMSNorm -> q8 (``out``)."""
+    launches.add()
+    kernels().tp_allreduce_rmsnorm_q8(x_in, x_out, tp.recv_local(site), tp.rank_stride, tp.world,
+                                       tp.counter_local(site), tp.epoch, producer_ctas, w, eps, out.q, out.d, out.s,
+                                       tp.status, PDL)
+
+
+def tp_argmax(tp, slots: torch.Tensor, rows: int, out: torch.Tensor):
+    """Global greedy ids from every rank's fused LM-head keys (vocabulary-parallel)."""
+    launches.add()
+    site = tp.argmax_site
+    kernels().tp_argmax(slots, rows, tp.max_rows, tp.keys_table, tp.base + tp.keys_off, tp.push_counters[site],
+                        tp.counter_local(site), tp.argmax_uses, tp.rank, out, tp.status, PDL)
 
 
 def argmax_finalize(slots: torch.Tensor, rows: int, out: torch.Tensor):

@@ -1,0 +1,157 @@
+"""`.gravity` mixed low-bit weights on the device (binary HGRAVB01, uniform HGRAVU01 2/4/8 bits).
+
+A ``MixedWeight`` holds one [N, K] tensor as two planes taken straight from the codec payload: the
+LSB-first code stream of every row and the fp16 group scales. ``MixedTable`` packs the device
+descriptors of many tensors (e.g. 512 experts x 3 matrices whose codecs differ per tensor) so one
+kernel launch can mix codecs. Quantisers here restate the codecs in PyTorch (device side) and are
+cross-checked against the C++ payload encoders/decoders.
+
+Parity: crates/hawking-core/src/model/qwen_complete_binary/q80_mixed_decode.rs (binary sign + mean-abs
+scale; uniform code = signed + bound, absmax / bound scale; LSB-first packing).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import List, Optional
+
+import numpy as np
+import torch
+
+from .._ext import kernels
+
+BINARY, UNIFORM = 0, 1
+
+
+def _pack_lsb(codes: torch.Tensor, bits: int) -> torch.Tensor:
+    """[N, K] small unsigned ints -> [N, K * bits / 8] bytes, LSB-first."""
+    N, K = codes.shape
+    per = 8 // bits
+    c = codes.to(torch.int32).reshape(N, K // per, per)
+    shifts = torch.arange(per, device=codes.device, dtype=torch.int32) * bits
+    return (c << shifts).sum(-1).to(torch.uint8)
+
+
+def _unpack_lsb(packed: torch.Tensor, bits: int, K: int) -> torch.Tensor:
+    N = packed.shape[0]
+    per = 8 // bits
+    shifts = torch.arange(per, device=packed.device, dtype=torch.int32) * bits
+    return ((packed.to(torch.int32).unsqueeze(-1) >> shifts) & ((1 << bits) - 1)).reshape(N, -1)[:, :K]
+
+
+@dataclass
+class MixedWeight:
+    kind: int
+    bits: int
+    group: int
+    N: int
+    K: int
+    codes: torch.Tensor   # uint8 [N, K * bits / 8]
+    scales: torch.Tensor  # fp16 [N, K / group]
+
+    @property
+    def bound(self) -> int:
+        return 0 if self.kind == BINARY else (1 << (self.bits - 1)) - 1
+
+    @property
+    def nbytes(self) -> int:
+        return self.codes.numel() + self.scales.numel() * 2
+
+    @property
+    def bpw(self) -> float:
+        return self.nbytes * 8.0 / (self.N * self.K)
+
+    # ---- construction ----
+    @staticmethod
+    def quantize(w: torch.Tensor, kind: int, bits: int = 1, group: int = 64) -> "MixedWeight":
+        """Encode fp32 [N, K] (any device) with the codec's own rule."""
+        N, K = w.shape
+        g = w.float().reshape(N, K // group, group)
+        if kind == BINARY:
+            scale = g.abs().mean(-1)
+            codes = (w >= 0).to(torch.uint8)
+            bits = 1
+        else:
+            bound = (1 << (bits - 1)) - 1
+            scale = g.abs().amax(-1) / bound
+            s16 = scale.to(torch.float16).float()
+            inv = torch.where(s16 > 0, 1.0 / s16, torch.zeros_like(s16))
+            codes = (torch.round(g * inv.unsqueeze(-1)).clamp(-bound, bound) + bound).reshape(N, K).to(torch.uint8)
+        return MixedWeight(kind, bits, group, N, K, _pack_lsb(codes, bits).contiguous(),
+                           scale.to(torch.float16).contiguous())
+
+    @staticmethod
+    def random(N: int, K: int, kind: int, bits: int, group: int, std: float, gen: torch.Generator, device) -> "MixedWeight":
+        """The codec of N(0, std) weights without materialising them: uniform random codes and
+        group scales at the statistics a Gaussian gives (benchmark weights)."""
+        bits = 1 if kind == BINARY else bits
+        codes = torch.randint(0, 256, (N, K * bits // 8), generator=gen, device=device, dtype=torch.int32).to(torch.uint8)
+        if kind == BINARY:
+            sc = std * 0.7979  # E|w| of a Gaussian
+        else:
+            bound = (1 << (bits - 1)) - 1
+            sc = std * 2.5 / bound  # ~ absmax of 64 Gaussian draws / bound
+            if bits == 2:  # codes 0..2 only
+                c = torch.randint(0, 3, (N, K), generator=gen, device=device, dtype=torch.int32)
+                codes = _pack_lsb(c, 2)
+        scales = torch.full((N, K // group), sc, dtype=torch.float16, device=device)
+        return MixedWeight(kind, bits, group, N, K, codes.contiguous(), scales)
+
+    @staticmethod
+    def from_payload(payload: np.ndarray, device) -> "MixedWeight":
+        """From an HGRAVB01 / HGRAVU01 envelope (bytes as in the artifact)."""
+        from ..formats import mixed as mx
+        magic, hdr, off, nbody = mx.header(payload)
+        rows, cols = int(hdr["shape"][0]), int(hdr["shape"][1])
+        gs = int(hdr["group_size"])
+        groups = rows * cols // gs
+        body = np.asarray(payload[off:off + nbody])
+        if magic == b"HGRAVB01":
+            kind, bits = BINARY, 1
+        elif magic == b"HGRAVU01":
+            kind, bits = UNIFORM, int(hdr["bits"])
+        else:
+            raise ValueError(f"no device layout for {magic!r}")
+        scales = torch.from_numpy(body[:groups * 2].copy().view(np.float16).reshape(rows, cols // gs))
+        codes = torch.from_numpy(body[groups * 2:].copy().reshape(rows, cols * bits // 8))
+        return MixedWeight(kind, bits, gs, rows, cols, codes.to(device).contiguous(), scales.to(device).contiguous())
+
+    def dequantize(self) -> torch.Tensor:
+        c = _unpack_lsb(self.codes, self.bits, self.K).float()
+        s = self.scales.float().repeat_interleave(self.group, 1)
+        if self.kind == BINARY:
+            return torch.where(c > 0, s, -s)
+        return (c - self.bound) * s
+
+    def rows(self, start: int, count: int) -> "MixedWeight":
+        return MixedWeight(self.kind, self.bits, self.group, count, self.K, self.codes[start:start + count],
+                           self.scales[start:start + count])
+
+
+class MixedTable:
+    """Device descriptor array over a list of MixedWeights (index i = weights[i])."""
+
+    def __init__(self, weights: List[MixedWeight]):
+        self.weights = list(weights)
+        self.descs = kernels().mixed_descs([w.codes for w in weights], [w.scales for w in weights],
+                                           [w.kind for w in weights], [w.bits for w in weights],
+                                           [w.group for w in weights])
+
+    @property
+    def nbytes(self) -> int:
+        return sum(w.nbytes for w in self.weights)
+
+
+def mixed_gemv(table: MixedTable, i: int, x, y: torch.Tensor, residual: bool = False, gate_logit=None):
+    from . import EPI_RESID, EPI_STORE, PDL, launches
+    w = table.weights[i]
+    launches.add()
+    kernels().mixed_gemv(EPI_RESID if residual else EPI_STORE, table.descs, i, i, w.N, w.K, x.q, x.d, x.s, y, 1.0,
+                         None, None, None, PDL, gate_logit)
+
+
+def mixed_gemv_swiglu(table: MixedTable, i_gate: int, i_up: int, x, out):
+    from . import EPI_SWIGLU_Q8, PDL, launches
+    w = table.weights[i_gate]
+    launches.add()
+    kernels().mixed_gemv(EPI_SWIGLU_Q8, table.descs, i_gate, i_up, w.N, w.K, x.q, x.d, x.s, None, 1.0, out.q, out.d,
+                         out.s, PDL, None)

@@ -1,0 +1,188 @@
+"""Tensor parallelism for the Llama family on the GPUs of one node.
+
+Sharding (rank r of N): Q/K/V heads split by head (column-parallel; every rank keeps its own KV
+heads in its own paged cache), gate/up split by FFN row, attention output and FFN down split along
+K (row-parallel: each rank produces a partial hidden vector), LM head split by vocabulary row, the
+embedding table replicated. Decode (GEMV path) all-reduces with the fused push kernels of
+``csrc/kernels/tp.cu``: the row-parallel GEMV stores its partial rows into every rank's receive
+region over NVLink and the next RMSNorm sums them; greedy sampling reduces per-rank (logit, index)
+keys the same way. Prefill (tensor-core path) all-reduces its partials with NCCL.
+
+``TPComm`` owns the shared buffers: one CUDA-IPC region per rank (receive regions of every
+all-reduce site, the argmax key region, arrival counters), mapped into every other rank's process.
+No NVLink multicast object is created.
+
+Parity: the reference has no tensor parallelism (one Apple GPU); the sharding plan follows the
+north-star requirement of column-parallel QKV/gate/up and row-parallel O/down with a vocabulary-
+parallel LM head.
+"""
+from __future__ import annotations
+
+from typing import List, Optional
+
+import torch
+import torch.distributed as dist
+
+from .._ext import kernels
+from ..formats.ggml import type_id
+from ..models.config import ModelConfig
+from ..ops.qweight import QWeight
+
+
+def local_config(cfg: ModelConfig, world: int) -> ModelConfig:
+    if cfg.n_heads % world or cfg.n_kv_heads % world or cfg.ffn % (32 * world):
+        raise ValueError(f"heads {cfg.n_heads}/{cfg.n_kv_heads} and ffn {cfg.ffn} must split over {world} ranks")
+    if cfg.vocab % world:
+        raise ValueError(f"vocab {cfg.vocab} must split over {world} ranks")
+    return cfg.with_(n_heads=cfg.n_heads // world, n_kv_heads=cfg.n_kv_heads // world, ffn=cfg.ffn // world)
+
+
+def cols(w: QWeight, k0: int, k1: int) -> QWeight:
+    """Columns [k0, k1) of an [N, K] block-format weight (whole blocks)."""
+    from ..formats.ggml import LAYOUTS
+    from ..ops.qweight import _PLANES
+    be = LAYOUTS[w.fmt].block_elems
+    if k0 % be or k1 % be:
+        raise ValueError("column slice must align to the format's blocks")
+    nb = w.K // be
+    planes = []
+    for p in w.planes:
+        pb = p.shape[1] // nb
+        planes.append(p.reshape(w.N, nb, pb)[:, k0 // be:k1 // be].reshape(w.N, -1).contiguous())
+    return QWeight(w.fmt, w.N, k1 - k0, planes)
+
+
+def shard_llama_weights(w, cfg: ModelConfig, rank: int, world: int):
+    """Rank ``rank``'s shard of full LlamaWeights (dense FFN layers)."""
+    from ..models.llama import LayerWeights, LlamaWeights
+    from ..ops.qweight import cat_rows
+    hd, nh, nkv, F = cfg.head_dim, cfg.n_heads, cfg.n_kv_heads, cfg.ffn
+    lnh, lnkv, lF = nh // world, nkv // world, F // world
+    layers = []
+    for lw in w.layers:
+        if lw.moe is not None:
+            raise NotImplementedError("tensor-parallel MoE layers: use expert parallelism")
+        qkv = lw.wqkv[0] if len(lw.wqkv) == 1 else cat_rows(lw.wqkv)
+        q = qkv.rows(rank * lnh * hd, lnh * hd)
+        k = qkv.rows(nh * hd + rank * lnkv * hd, lnkv * hd)
+        v = qkv.rows((nh + nkv) * hd + rank * lnkv * hd, lnkv * hd)
+        nl = LayerWeights(attn_norm=lw.attn_norm, wqkv=[cat_rows([q, k, v])],
+                          wo=cols(lw.wo, rank * lnh * hd, (rank + 1) * lnh * hd), ffn_norm=lw.ffn_norm)
+        if lw.qkv_bias is not None:
+            b = lw.qkv_bias
+            nl.qkv_bias = torch.cat([b[rank * lnh * hd:(rank + 1) * lnh * hd],
+                                     b[nh * hd + rank * lnkv * hd:nh * hd + (rank + 1) * lnkv * hd],
+                                     b[(nh + nkv) * hd + rank * lnkv * hd:(nh + nkv) * hd + (rank + 1) * lnkv * hd]])
+        nl.q_norm, nl.k_norm = lw.q_norm, lw.k_norm
+        gate, up = lw.w_gate.rows(rank * lF, lF), lw.w_up.rows(rank * lF, lF)
+        nl.w_gu = cat_rows([gate, up])
+        nl.w_gate, nl.w_up = nl.w_gu.rows(0, lF), nl.w_gu.rows(lF, lF)
+        nl.w_down = cols(lw.w_down, rank * lF, (rank + 1) * lF)
+        layers.append(nl)
+    V = w.lm_head.N
+    head = w.lm_head.rows(rank * (V // world), V // world)
+    head = QWeight(head.fmt, head.N, head.K, [p.contiguous() for p in head.planes])
+    return LlamaWeights(embed=w.embed, out_norm=w.out_norm, lm_head=head, layers=layers, rope_freqs=w.rope_freqs)
+
+
+def random_llama_weights_tp(cfg: ModelConfig, rank: int, world: int, device, seed: int = 0, std: float = 0.02):
+    """Random-init weights generated directly in rank ``rank``'s shard shapes (benchmarks)."""
+    from ..models.llama import LayerWeights, LlamaWeights
+    g = torch.Generator(device=device)
+    g.manual_seed(seed * 1009 + rank)
+    fmt = type_id(cfg.weight_type)
+    efmt = type_id(cfg.embed_type or cfg.weight_type)
+    H, hd = cfg.hidden, cfg.head_dim
+    lnh, lnkv, lF = cfg.n_heads // world, cfg.n_kv_heads // world, cfg.ffn // world
+
+    def W(N, K, f=fmt):
+        return QWeight.random(f, N, K, std, g, device)
+
+    layers = []
+    for _ in range(cfg.layers):
+        lw = LayerWeights(attn_norm=torch.ones(H, device=device), wqkv=[W((lnh + 2 * lnkv) * hd, H)],
+                          wo=W(H, lnh * hd), ffn_norm=torch.ones(H, device=device))
+        gu = W(2 * lF, H)
+        lw.w_gu, lw.w_gate, lw.w_up = gu, gu.rows(0, lF), gu.rows(lF, lF)
+        lw.w_down = W(H, lF)
+        layers.append(lw)
+    g2 = torch.Generator(device=device)
+    g2.manual_seed(seed * 1009 + 7777)  # the replicated embedding is identical on every rank
+    embed = QWeight.random(efmt, cfg.vocab, H, std, g2, device)
+    head = W(cfg.vocab // world, H)
+    torch.cuda.synchronize(device)
+    return LlamaWeights(embed=embed, out_norm=torch.ones(H, device=device), lm_head=head, layers=layers)
+
+
+class TPComm:
+    """Shared buffers and pointer tables of the fused collectives for one rank."""
+
+    def __init__(self, rank: int, world: int, n_sites: int, max_rows: int, width: int, device,
+                 group: Optional[dist.ProcessGroup] = None):
+        K = kernels()
+        self.rank, self.world, self.n_sites = rank, world, n_sites
+        self.max_rows, self.width = max_rows, width
+        self.dev = torch.device(device)
+        self.group = group
+        self.rank_stride = max_rows * width                       # floats per source rank
+        self.site_floats = world * self.rank_stride
+        recv_bytes = n_sites * self.site_floats * 4
+        self.keys_off = recv_bytes
+        keys_bytes = world * max_rows * 8
+        self.cnt_off = self.keys_off + keys_bytes
+        total = self.cnt_off + (n_sites + 1) * 8
+        total = (total + 255) // 256 * 256
+        with torch.cuda.device(self.dev):
+            self.base = K.ipc_malloc(total)
+            handle = bytes(K.ipc_handle(self.base))
+        handles: List[bytes] = [None] * world
+        dist.all_gather_object(handles, handle, group=group)
+        self.ptrs = []
+        with torch.cuda.device(self.dev):
+            for p, h in enumerate(handles):
+                self.ptrs.append(self.base if p == rank else K.ipc_open(h))
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=self.dev)       # forwards on the push path
+        self.argmax_uses = torch.zeros(1, dtype=torch.int32, device=self.dev)  # greedy rounds
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.dev)
+
+        def table(vals):
+            return torch.tensor(vals, dtype=torch.int64, device=self.dev)
+
+        # per site: where MY partial goes in every rank's region, and every rank's counter
+        self.push_recv = [table([self.ptrs[p] + 4 * (s * self.site_floats + rank * self.rank_stride)
+                                 for p in range(world)]) for s in range(n_sites)]
+        self.push_counters = [table([self.ptrs[p] + self.cnt_off + 8 * s for p in range(world)])
+                              for s in range(n_sites + 1)]
+        self.keys_table = table([self.ptrs[p] + self.keys_off for p in range(world)])
+        self.closed = False
+
+    # local addresses
+    def recv_local(self, site: int) -> int:
+        return self.base + 4 * site * self.site_floats
+
+    def counter_local(self, site: int) -> int:
+        return self.base + self.cnt_off + 8 * site
+
+    @property
+    def argmax_site(self) -> int:
+        return self.n_sites
+
+    def check(self):
+        st = int(self.status.item())
+        if st:
+            raise RuntimeError(f"tensor-parallel collective reported device error {st} (peer timeout)")
+
+    def close(self):
+        if self.closed:
+            return
+        torch.cuda.synchronize(self.dev)
+        dist.barrier(group=self.group)
+        K = kernels()
+        with torch.cuda.device(self.dev):
+            for p, ptr in enumerate(self.ptrs):
+                if p != self.rank:
+                    K.ipc_close(ptr)
+        dist.barrier(group=self.group)
+        with torch.cuda.device(self.dev):
+            K.ipc_free(self.base)
+        self.closed = True

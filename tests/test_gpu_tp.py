@@ -1,0 +1,79 @@
+"""Tensor parallelism on 2 GPUs (one process per GPU, NCCL plumbing): the fused push all-reduce
+and vocabulary-parallel greedy give the TP=1 logits and tokens.
+
+Runs only where at least two GPUs are visible."""
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, gguf, out_path):
+    import datetime
+
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        from hawking_b200.engine.engine import Engine
+        from hawking_b200.engine.sampling import SamplingParams
+        from hawking_b200.formats.gguf import GgufModel
+        from hawking_b200.models.llama import load_llama_weights
+        from hawking_b200.models.torch_ref import config_from_gguf
+        from hawking_b200.parallel.tp import TPComm, local_config, shard_llama_weights
+        m = GgufModel(gguf)
+        cfg = config_from_gguf(m).with_(max_ctx=128)
+        w = load_llama_weights(m, cfg, dev)
+        tp = TPComm(rank, world, 2 * cfg.layers, 8, cfg.hidden, dev)
+        eng = Engine.build(local_config(cfg, world), shard_llama_weights(w, cfg, rank, world), device=dev,
+                           max_batch=2, max_ctx=128, block_size=16, num_blocks=64, max_rows=8, tp=tp)
+        toks = list(range(10, 22))
+        local = eng.model.forward_tokens(toks, seq_id=1)
+        eng.kv.drop(1)
+        parts = [torch.empty_like(local) for _ in range(world)]
+        dist.all_gather(parts, local.contiguous())
+        full = torch.cat(parts, 1)
+        gen = eng.generate([list(range(30, 40))], SamplingParams(max_tokens=6))[0]
+        gens = [None] * world
+        dist.all_gather_object(gens, gen)
+        tp.check()
+        if rank == 0:
+            ref = Engine.build(cfg, w, device=dev, max_batch=2, max_ctx=128, block_size=16, num_blocks=64, max_rows=8)
+            ref_logits = ref.model.forward_tokens(toks, seq_id=1)
+            ref_gen = ref.generate([list(range(30, 40))], SamplingParams(max_tokens=6))[0]
+            err = float((full - ref_logits).abs().max() / ref_logits.abs().max())
+            agree = float((full.argmax(1) == ref_logits.argmax(1)).float().mean())
+            torch.save({"err": err, "agree": agree, "gens": gens, "ref_gen": ref_gen}, out_path)
+        torch.cuda.synchronize()
+        tp.close()
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp2_matches_tp1(tiny_gguf, tmp_path):
+    import torch.multiprocessing as mp
+    out = str(tmp_path / "tp.pt")
+    mp.spawn(_worker, args=(2, _free_port(), tiny_gguf, out), nprocs=2, join=True)
+    r = torch.load(out)
+    assert r["err"] < 0.03, r
+    assert r["agree"] >= 0.9, r
+    assert r["gens"][0] == r["gens"][1]  # every rank decodes the same tokens
+    assert r["gens"][0][0] == r["ref_gen"][0]
