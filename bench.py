@@ -58,12 +58,98 @@ def reference_unavailable(args):
     print(json.dumps(line))
 
 
+def bench_qwen_next(args):
+    """Qwen3-Next-style hybrid (config 4): bs1 / bs8 device-timed decode on one GPU, 80B-parameter
+    random weights in the mixed <= 1.5 BPW recipe (random codes + Gaussian-statistics scales)."""
+    import torch
+    from hawking_b200.engine.kv_cache import PagedKVCache
+    from hawking_b200.models.config import preset
+    from hawking_b200.models.qwen_next import QwenNextModel, random_qwen_next_weights
+    from hawking_b200.utils.clocks import ClockSampler
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    K, W, ctx = args.steps, args.warmup, args.ctx
+    cfg = preset("qwen3-next", max_ctx=ctx + 2 * (K + W) + 64)
+    if args.layers:
+        cfg = cfg.with_(layers=args.layers)
+    t0 = time.time()
+    w = random_qwen_next_weights(cfg, dev, seed=0)
+    t_load = time.time() - t0
+    n_full = sum(cfg.layer_is_full_attention(l) for l in range(cfg.layers))
+    bs, max_seqs = 64, 8
+    max_blocks = -(-cfg.max_ctx // bs)
+    kv = PagedKVCache(n_full, cfg.n_kv_heads, cfg.head_dim, max_seqs * max_blocks + 8, bs, max_seqs, max_blocks, dev)
+    m = QwenNextModel(cfg, w, kv, max_rows=8, max_seqs=max_seqs, device=dev)
+    g = torch.Generator(device=dev).manual_seed(1)
+    for l in range(n_full):
+        kv.k[l].normal_(0, 1, generator=g)
+        kv.v[l].normal_(0, 1, generator=g)
+    m.ssm_state.normal_(0, 0.05, generator=g)
+    m.conv_state.normal_(0, 0.5, generator=g)
+    elements = sum(t.N * t.K for t in w.table.weights) + w.embed.N * w.embed.K
+    complete_bpw = (w.table.nbytes + w.embed.nbytes) * 8.0 / elements
+    expert_bytes = sum(t.nbytes for t in w.table.weights if t.N * t.K == cfg.expert_ffn * cfg.hidden)
+
+    def timed(nseq):
+        ids, pos, rseq, rctx = [], [], [], []
+        for i in range(nseq):
+            sid = 10 + i
+            kv.bm.reserve(sid, ctx + K + W + 8)
+            kv.sync_tables([sid])
+            ids.append(int(torch.randint(0, cfg.vocab, (1,)).item()))
+            pos.append(ctx)
+            rseq.append(kv.row(sid))
+            rctx.append(ctx + 1)
+        m.inp.upload(ids, pos, [0] * nseq, rseq, rctx)
+        for _ in range(W):
+            m.graph_forward(nseq, "greedy", advance=True)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(0, period_ms=50) as cs:
+            e0.record()
+            for _ in range(K):
+                m.graph_forward(nseq, "greedy", advance=True)
+            e1.record()
+            torch.cuda.synchronize()
+        for i in range(nseq):
+            kv.drop(10 + i)
+        return e0.elapsed_time(e1) / K, cs.result
+
+    ms1, clocks = timed(1)
+    launches = m.launches_per_graph
+    ms8, clocks8 = timed(8)
+    out = {
+        "metric": "decode tok/s bs1 (Qwen3-Next-style hybrid MoE, .gravity mixed <= 1.5 BPW), 1 GPU",
+        "value": round(1000.0 / ms1, 2), "unit": "tok/s", "n_gpus": 1, "steps": K, "warmup": W,
+        "ms_per_step": round(ms1, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "binary/ternary experts and Q4 projections (per-64 fp16 group scales) x int8 activation blocks, "
+                 "fp32 accumulate and DeltaNet state, bf16 KV",
+        "data": "synthetic: random codes with Gaussian-statistics group scales (80B-parameter model), random KV "
+                "and recurrent state for a %d-token context, uniform-random token ids" % ctx,
+        "config": {"model": "qwen3-next (48 layers, hidden 2048, 12 gated full-attention layers 16/2 heads hd 256, "
+                            "36 gated DeltaNet layers 16k/32v heads hd 128, 512 experts top-10 + shared, FFN 512, "
+                            "vocab 151936)" + (f" [LAYERS OVERRIDDEN to {cfg.layers}]" if args.layers else ""),
+                   "global_batch": 1, "seq_len": ctx, "parallelism": "tp1",
+                   "complete_bpw": round(complete_bpw, 3),
+                   "l2": "inputs larger than L2: %.1f GB of weights resident" % ((w.table.nbytes + w.embed.nbytes) / 1e9)},
+        "clocks": clocks, "e2e": None, "e2e_note": "no engine/scheduler integration for the hybrid model yet",
+        "gpu_launches": launches * K,
+        "bs8": {"tok_s_aggregate": round(8 * 1000.0 / ms8, 1), "ms_per_step": round(ms8, 4), "clocks": clocks8},
+        "weights_gb": round((w.table.nbytes + w.embed.nbytes) / 1e9, 2),
+        "expert_weights_gb": round(expert_bytes / 1e9, 2), "load_s": round(t_load, 1),
+    }
+    print(json.dumps(out))
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         if int(os.environ.get("RANK", "0")) == 0:
             reference_unavailable(args)
         return 0
+    if args.model == "qwen3-next":
+        return bench_qwen_next(args)
 
     import torch
     import torch.distributed as dist

@@ -185,10 +185,87 @@ void sigmoid_gate_q8(const Tensor& o, const Tensor& gate, const Tensor& oq, cons
   hk::sigmoid_gate_q8_launch(ptr<float>(o), ptr<float>(gate), gate.stride(0), (int)o.size(0), (int)o.size(1),
                              ptr<int8_t>(oq), ptr<float>(od), ptr<float>(os), cur_stream(), pdl);
 }
+void mla_kv_append(const Tensor& kv_a, const Tensor& norm_w, double eps, const Tensor& positions,
+                   const Tensor& block_tables, const Tensor& row_seq, const Tensor& rope, const Tensor& cache, bool pdl) {
+  hk::MlaAppendArgs a{};
+  a.kv_a = ptr<float>(kv_a);
+  a.kv_a_stride = kv_a.stride(0);
+  a.norm_w = ptr<float>(norm_w);
+  a.eps = (float)eps;
+  a.positions = ptr<int>(positions);
+  a.block_tables = ptr<int>(block_tables);
+  a.row_seq = ptr<int>(row_seq);
+  a.max_blocks = (int)block_tables.size(1);
+  a.block_size = (int)cache.size(1);
+  a.rope = ptr<float>(rope);
+  a.cache = ptr<__nv_bfloat16>(cache);
+  TORCH_CHECK(cache.scalar_type() == at::kBFloat16 && cache.size(2) == 576, "mla cache: bf16 [blocks, bs, 576]");
+  const c10::cuda::CUDAGuard g(kv_a.device());
+  hk::mla_kv_append_launch(a, (int)kv_a.size(0), cur_stream(), pdl);
+}
+
+void mla_absorb_q(const Tensor& q, const Tensor& w_uk, const Tensor& positions, const Tensor& rope, const Tensor& q_lat,
+                  const Tensor& q_pe, bool pdl) {
+  hk::MlaAbsorbArgs a{};
+  a.q = ptr<float>(q);
+  a.w_uk = ptr<__nv_bfloat16>(w_uk);
+  a.positions = ptr<int>(positions);
+  a.rope = ptr<float>(rope);
+  a.nh = (int)w_uk.size(0);
+  a.nope = (int)w_uk.size(1);
+  a.q_lat = ptr<float>(q_lat);
+  a.q_pe = ptr<float>(q_pe);
+  const c10::cuda::CUDAGuard g(q.device());
+  hk::mla_absorb_q_launch(a, (int)q.size(0), cur_stream(), pdl);
+}
+
+void mla_decode(const Tensor& q_lat, const Tensor& q_pe, const Tensor& cache, const Tensor& block_tables,
+                const Tensor& row_seq, const Tensor& row_ctx, double scale, int64_t num_splits, const Tensor& o_lat,
+                const Tensor& status, bool pdl) {
+  hk::MlaDecodeArgs a{};
+  a.q_lat = ptr<float>(q_lat);
+  a.q_pe = ptr<float>(q_pe);
+  a.cache = ptr<__nv_bfloat16>(cache);
+  a.block_tables = ptr<int>(block_tables);
+  a.max_blocks = (int)block_tables.size(1);
+  a.row_seq = ptr<int>(row_seq);
+  a.row_ctx = ptr<int>(row_ctx);
+  a.scale = (float)scale;
+  a.R = (int)q_lat.size(0);
+  a.nh = (int)q_lat.size(1);
+  a.block_size = (int)cache.size(1);
+  a.num_splits = (int)num_splits;
+  a.o_lat = ptr<float>(o_lat);
+  a.status = ptr<int>(status);
+  const c10::cuda::CUDAGuard g(q_lat.device());
+  hk::mla_decode_launch(a, cur_stream(), pdl);
+}
+
+void mla_out(const Tensor& o_lat, const Tensor& w_uv, const Tensor& oq, const Tensor& od, const Tensor& os, bool pdl) {
+  hk::MlaOutArgs a{};
+  a.o_lat = ptr<float>(o_lat);
+  a.w_uv = ptr<__nv_bfloat16>(w_uv);
+  a.nh = (int)w_uv.size(0);
+  a.vdim = (int)w_uv.size(1);
+  a.oq = ptr<int8_t>(oq);
+  a.od = ptr<float>(od);
+  a.os = ptr<float>(os);
+  const c10::cuda::CUDAGuard g(o_lat.device());
+  hk::mla_out_launch(a, (int)o_lat.size(0), cur_stream(), pdl);
+}
 }  // namespace
 
 namespace hk {
 void register_model_kernels(py::module_& m) {
+  m.def("mla_kv_append", &mla_kv_append, py::arg("kv_a"), py::arg("norm_w"), py::arg("eps"), py::arg("positions"),
+        py::arg("block_tables"), py::arg("row_seq"), py::arg("rope"), py::arg("cache"), py::arg("pdl") = false);
+  m.def("mla_absorb_q", &mla_absorb_q, py::arg("q"), py::arg("w_uk"), py::arg("positions"), py::arg("rope"),
+        py::arg("q_lat"), py::arg("q_pe"), py::arg("pdl") = false);
+  m.def("mla_decode", &mla_decode, py::arg("q_lat"), py::arg("q_pe"), py::arg("cache"), py::arg("block_tables"),
+        py::arg("row_seq"), py::arg("row_ctx"), py::arg("scale"), py::arg("num_splits"), py::arg("o_lat"),
+        py::arg("status"), py::arg("pdl") = false);
+  m.def("mla_out", &mla_out, py::arg("o_lat"), py::arg("w_uv"), py::arg("oq"), py::arg("od"), py::arg("os"),
+        py::arg("pdl") = false);
   m.def("mixed_descs", &mixed_descs);
   m.def("mixed_gemv", &mixed_gemv, py::arg("epi"), py::arg("descs"), py::arg("d0"), py::arg("d1"), py::arg("N"),
         py::arg("K"), py::arg("xq"), py::arg("xd"), py::arg("xs"), py::arg("y") = py::none(), py::arg("alpha") = 1.0,

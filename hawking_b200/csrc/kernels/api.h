@@ -360,6 +360,54 @@ void deltanet_recurrent_launch(const DeltaRecArgs& a, int n_value_heads, int row
 void sigmoid_gate_q8_launch(const float* o, const float* gate, int64_t gate_stride, int rows, int W, int8_t* oq,
                             float* od, float* os, cudaStream_t s, bool pdl);
 
+// ---- MLA (mla.cu) ----
+struct MlaAppendArgs {
+  const float* kv_a;          // [R, kv_a_stride]: latent (512) then k_pe (64), pre-norm / pre-RoPE
+  int64_t kv_a_stride;
+  const float* norm_w;        // [512] kv_a RMSNorm weight
+  float eps;
+  const int* positions;
+  const int* block_tables;
+  const int* row_seq;
+  int max_blocks, block_size;
+  const float* rope;          // [max_pos, 32, 2] (cos, sin) over the 64 rope dims
+  __nv_bfloat16* cache;       // [num_blocks, block_size, 576]
+};
+void mla_kv_append_launch(const MlaAppendArgs& a, int rows, cudaStream_t s, bool pdl);
+struct MlaAbsorbArgs {
+  const float* q;             // [R, nh, nope + 64]
+  const __nv_bfloat16* w_uk;  // [nh, nope, 512]
+  const int* positions;
+  const float* rope;
+  int nh, nope;
+  float* q_lat;               // [R, nh, 512]
+  float* q_pe;                // [R, nh, 64]
+};
+void mla_absorb_q_launch(const MlaAbsorbArgs& a, int rows, cudaStream_t s, bool pdl);
+struct MlaDecodeArgs {
+  const float* q_lat;
+  const float* q_pe;
+  const __nv_bfloat16* cache;
+  const int* block_tables;
+  int max_blocks;
+  const int* row_seq;
+  const int* row_ctx;
+  float scale;
+  int R, nh, block_size, num_splits, stage_blocks;
+  float* o_lat;               // [R, nh, 512]
+  int* status;
+};
+void mla_decode_launch(MlaDecodeArgs a, cudaStream_t s, bool pdl);
+struct MlaOutArgs {
+  const float* o_lat;
+  const __nv_bfloat16* w_uv;  // [nh, vdim, 512]
+  int nh, vdim;
+  int8_t* oq;                 // q8 [R, nh * vdim]
+  float* od;
+  float* os;
+};
+void mla_out_launch(const MlaOutArgs& a, int rows, cudaStream_t s, bool pdl);
+
 // ---- quantisers (quantize.cu) ----
 // n elements (rows * cols, cols a multiple of the block) -> planes p0..p3 of format fmt.
 void quantize_launch(int fmt, const float* x, int64_t n, void* p0, void* p1, void* p2, void* p3, cudaStream_t s);
