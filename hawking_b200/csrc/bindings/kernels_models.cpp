@@ -28,19 +28,24 @@ Tensor mixed_descs(const std::vector<Tensor>& codes, const std::vector<Tensor>& 
   std::vector<hk::MixedDesc> h(n);
   for (size_t i = 0; i < n; ++i) {
     TORCH_CHECK(codes[i].is_cuda() && codes[i].scalar_type() == at::kByte && codes[i].dim() == 2, "codes: uint8 [rows, bytes]");
-    TORCH_CHECK(scales[i].is_cuda() && scales[i].scalar_type() == at::kHalf && scales[i].dim() == 2, "scales: fp16 [rows, groups]");
+    const bool fp8 = kind[i] == hk::MIXED_FP8;
+    TORCH_CHECK(scales[i].is_cuda() && scales[i].scalar_type() == (fp8 ? at::kFloat : at::kHalf) && scales[i].dim() == 2,
+                "scales: fp16 (fp32 for fp8) [rows, groups]");
     TORCH_CHECK((reinterpret_cast<uintptr_t>(codes[i].data_ptr()) & 15) == 0 && codes[i].stride(0) % 16 == 0,
                 "codes rows must be 16-byte aligned");
     h[i].codes = ptr<uint8_t>(codes[i]);
-    h[i].scales = ptr<__half>(scales[i]);
+    h[i].scales = fp8 ? nullptr : ptr<__half>(scales[i]);
+    h[i].scales_f32 = fp8 ? ptr<float>(scales[i]) : nullptr;
     h[i].code_row_bytes = codes[i].stride(0);
     h[i].scale_row_elems = scales[i].stride(0);
     h[i].kind = (int)kind[i];
     h[i].bits = (int)bits[i];
     h[i].group = (int)group[i];
-    h[i].bound = kind[i] == hk::MIXED_BINARY ? 0 : (1 << (bits[i] - 1)) - 1;
-    TORCH_CHECK(kind[i] == hk::MIXED_BINARY ? bits[i] == 1 : (bits[i] == 2 || bits[i] == 4 || bits[i] == 8),
-                "mixed codec: binary (1 bit) or uniform 2/4/8 bits");
+    h[i].bound = kind[i] == hk::MIXED_UNIFORM ? (1 << (bits[i] - 1)) - 1 : 0;
+    TORCH_CHECK(kind[i] == hk::MIXED_BINARY ? bits[i] == 1
+                                            : (kind[i] == hk::MIXED_FP8 ? bits[i] == 8
+                                                                        : (bits[i] == 2 || bits[i] == 4 || bits[i] == 8)),
+                "mixed codec: binary (1 bit), uniform 2/4/8 bits or fp8 (8 bits)");
     TORCH_CHECK(group[i] % 32 == 0, "mixed codec: group must be a multiple of 32");
   }
   Tensor out = torch::empty({(int64_t)(n * sizeof(hk::MixedDesc))},

@@ -273,10 +273,11 @@ struct MoeGemvArgs {
 void moe_gemv_launch(int fmt, int epi, const MoeGemvArgs& a, cudaStream_t s, bool pdl);
 
 // ---- `.gravity` mixed low-bit codecs (mixed_gemv.cu) ----
-enum MixedKind : int { MIXED_BINARY = 0, MIXED_UNIFORM = 1 };
+enum MixedKind : int { MIXED_BINARY = 0, MIXED_UNIFORM = 1, MIXED_FP8 = 2 };
 struct MixedDesc {            // one weight tensor [rows, K] in device memory
   const uint8_t* codes;       // LSB-first code stream per row
-  const __half* scales;       // fp16 group scales per row
+  const __half* scales;       // fp16 group scales per row (binary / uniform)
+  const float* scales_f32;    // fp8: fp32 scale per (row, group of columns)
   int64_t code_row_bytes;     // K * bits / 8
   int64_t scale_row_elems;    // K / group
   int kind, bits, group, bound;

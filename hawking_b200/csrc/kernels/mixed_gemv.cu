@@ -23,6 +23,8 @@
 // (binary / uniform matvec oracles), crates/hawking-core/shaders/q80_mixed_decode.metal and
 // qwen_uniform_q4.metal / qwen_binary*.metal (packed matvec families),
 // qwen80_all_ten_routed_expert_wave.metal (10 routed experts through a 512-way expert table).
+#include <cuda_fp8.h>
+
 #include "api.h"
 #include "qformats.cuh"
 
@@ -39,11 +41,30 @@ __device__ __forceinline__ uint32_t spread2(uint32_t byte) {
 __device__ __forceinline__ float mixed_block_dot(const MixedDesc& t, int64_t row, int blk, const int8_t* xq,
                                                   float dx, float sx) {
   const uint8_t* codes = t.codes + row * t.code_row_bytes;
-  const float sg = __half2float(t.scales[row * t.scale_row_elems + (blk * 32) / t.group]);
+  const float sg = t.kind == MIXED_FP8 ? 0.f : __half2float(t.scales[row * t.scale_row_elems + (blk * 32) / t.group]);
   const int4 qa = *reinterpret_cast<const int4*>(xq + blk * 32);
   const int4 qb = *reinterpret_cast<const int4*>(xq + blk * 32 + 16);
   const int q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
   int dot = 0;
+  if (t.kind == MIXED_FP8) {  // fp8 e4m3 codes, fp32 scale per 128-column block of the row
+    const float sw = t.scales_f32[row * t.scale_row_elems + (blk * 32) / t.group];
+    const uint4 w0 = __ldg(reinterpret_cast<const uint4*>(codes) + 2 * blk);
+    const uint4 w1 = __ldg(reinterpret_cast<const uint4*>(codes) + 2 * blk + 1);
+    const uint32_t ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    float acc = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const __half2_raw lo = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(ws[j] & 0xFFFFu), __NV_E4M3);
+      const __half2_raw hi = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(ws[j] >> 16), __NV_E4M3);
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&lo));
+      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&hi));
+      const uint32_t qw = (uint32_t)q[j];
+      acc += a.x * (float)(int8_t)(qw & 0xFF) + a.y * (float)(int8_t)((qw >> 8) & 0xFF) +
+             b.x * (float)(int8_t)((qw >> 16) & 0xFF) + b.y * (float)(int8_t)(qw >> 24);
+    }
+    (void)sx;
+    return sw * dx * acc;
+  }
   if (t.kind == MIXED_BINARY) {
     const uint32_t b = __ldg(reinterpret_cast<const uint32_t*>(codes) + blk);
 #pragma unroll

@@ -148,7 +148,7 @@ void mla_out_launch(const MlaOutArgs& a, int rows, cudaStream_t s, bool pdl) {
 // ---- attention over the latent cache --------------------------------------------------------
 template <int G, int WARPS>
 __global__ void __launch_bounds__(WARPS * 32) mla_decode_kernel(MlaDecodeArgs a) {
-  constexpr int T = 32 / G > 8 ? 8 : 32 / G;
+  constexpr int T = 16 / G > 4 ? 4 : 16 / G;  // tokens per warp tile (register budget: 18 dims per token)
   constexpr int NV = G * T;
   constexpr int NQ = kMlaRow / 32;   // 18 score dims per lane
   constexpr int NO = kMlaLat / 32;   // 16 value dims per lane
@@ -234,7 +234,7 @@ __global__ void __launch_bounds__(WARPS * 32) mla_decode_kernel(MlaDecodeArgs a)
       for (int j = 0; j < T; ++j) {
         const int t = min(tt + j, tw1 - 1);
         const __nv_bfloat16* row = base + (int64_t)(t - wb0 * bs) * kMlaRow;
-        float kr[NQ];
+        float kr[NQ];  // (loaded per token)
 #pragma unroll
         for (int i = 0; i < NQ; ++i) kr[i] = __bfloat162float(row[lane + 32 * i]);
 #pragma unroll

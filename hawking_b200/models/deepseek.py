@@ -1,0 +1,370 @@
+"""DeepSeek-V3-style MLA + MoE decoder with fp8 e4m3 block-scaled weights.
+
+Attention is multi-head latent attention: the query goes through a low-rank q_a -> RMSNorm -> q_b;
+the key/value through kv_a -> (RMSNorm'd 512-d latent, 64-d RoPE key) that is all the paged cache
+holds; the key and value up-projections are absorbed into the query (q_lat = W_UK^T q_nope) and the
+output (o = W_UV o_lat), so decode attends directly over the latent cache (K6 kernels). The first
+``first_dense_layers`` layers have a dense SwiGLU FFN; the rest route each token to top-k of many
+experts with sigmoid scores plus a learned selection bias, group-limited selection, renormalised
+and scaled weights, plus one shared expert. Every projection matrix is fp8 e4m3 with 128 x 128
+block scales (K1 fp8 path of the mixed GEMV kernels); W_UK / W_UV are kept in bf16.
+
+Decode runs rows <= 8 through the GEMV path; prompts are fed through the same path in chunks of up
+to 8 tokens of one sequence (the latent cache makes multi-row prefill exact).
+
+Parity: crates/hawking-core/src/model/deepseek_v2.rs:72-158 (config: q_lora, kv_lora 512, rope 64,
+nope 128, v 128, routed + shared experts, first_k_dense), :2170 (forward_token), crates/hawking-core/
+src/attn.rs:185 (mla_decode_step), crates/hawking-core/src/moe.rs:24 (top-k gate),
+crates/hawking-core/shaders/attn.metal:18-47 (absorbed MLA decode).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional
+
+import torch
+
+from .. import ops
+from .._ext import kernels
+from ..ops import Q8Act, QWeight
+from ..ops.mixed import MixedTable, MixedWeight, mixed_gemv, mixed_gemv_swiglu
+from .config import ModelConfig
+
+LAT, ROPE = 512, 64
+
+
+@dataclass
+class DSLayer:
+    dense: bool
+    attn_norm: torch.Tensor
+    q_a_norm: torch.Tensor
+    kv_a_norm: torch.Tensor
+    ffn_norm: torch.Tensor
+    w_uk: torch.Tensor                  # bf16 [nh, nope, 512]
+    w_uv: torch.Tensor                  # bf16 [nh, v, 512]
+    idx: Dict[str, int] = field(default_factory=dict)
+    router: Optional[torch.Tensor] = None
+    router_bias: Optional[torch.Tensor] = None
+
+
+@dataclass
+class DSWeights:
+    table: MixedTable
+    embed: QWeight
+    out_norm: torch.Tensor
+    layers: List[DSLayer]
+    lm_head: int
+
+    @property
+    def nbytes(self) -> int:
+        n = self.table.nbytes + self.embed.nbytes
+        for l in self.layers:
+            n += (l.w_uk.numel() + l.w_uv.numel()) * 2
+            if l.router is not None:
+                n += l.router.numel() * 4
+        return n
+
+
+def random_deepseek_weights(cfg: ModelConfig, device, seed: int = 0, std: float = 0.02,
+                            materialise: bool = True) -> DSWeights:
+    """Random-init fp8 weights. ``materialise`` quantises Gaussian weights tile by tile (exact
+    recipe); the kernels see identical layouts either way."""
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    H, nh, V = cfg.hidden, cfg.n_heads, cfg.vocab
+    nope, rd, vd = cfg.qk_nope_dim, cfg.qk_rope_dim, cfg.v_head_dim
+    ws: List[MixedWeight] = []
+
+    def add(N, K):
+        ws.append(MixedWeight.random_fp8(N, K, std, g, device))
+        return len(ws) - 1
+
+    def ones(n):
+        return torch.ones(n, device=device)
+
+    layers = []
+    for l in range(cfg.layers):
+        dense = l < cfg.first_dense_layers
+        L = DSLayer(dense, ones(H), ones(cfg.q_lora_rank), ones(LAT), ones(H),
+                    w_uk=(torch.randn(nh, nope, LAT, generator=g, device=device) * std).bfloat16(),
+                    w_uv=(torch.randn(nh, vd, LAT, generator=g, device=device) * std).bfloat16())
+        L.idx["qa"] = add(cfg.q_lora_rank, H)
+        L.idx["qb"] = add(nh * (nope + rd), cfg.q_lora_rank)
+        L.idx["kva"] = add(LAT + ROPE, H)
+        L.idx["o"] = add(H, nh * vd)
+        if dense:
+            L.idx["g"] = add(cfg.ffn, H)
+            L.idx["u"] = add(cfg.ffn, H)
+            L.idx["d"] = add(H, cfg.ffn)
+        else:
+            E, F = cfg.n_experts, cfg.expert_ffn
+            L.router = torch.randn(E, H, generator=g, device=device) * std
+            L.router_bias = torch.randn(E, generator=g, device=device) * 0.01
+            for m, (n, k) in (("eg", (F, H)), ("eu", (F, H)), ("ed", (H, F))):
+                # all experts of one matrix drawn at once, then viewed per expert
+                stacked = MixedWeight.random_fp8(E * n, k, std, g, device)
+                L.idx[m] = len(ws)
+                for e in range(E):
+                    ws.append(stacked.rows(e * n, n))
+            L.idx["sg"] = add(cfg.shared_ffn, H)
+            L.idx["su"] = add(cfg.shared_ffn, H)
+            L.idx["sd"] = add(H, cfg.shared_ffn)
+        layers.append(L)
+    head = add(V, H)
+    emb = QWeight.quantize(torch.randn(V, H, generator=g, device=device) * std, 1)  # F16 table
+    torch.cuda.synchronize(device)
+    return DSWeights(MixedTable(ws), emb, ones(H), layers, head)
+
+
+class DeepSeekModel:
+    """Decode forward over static buffers (rows <= 8)."""
+
+    def __init__(self, cfg: ModelConfig, w: DSWeights, kv, max_rows: int = 8, device="cuda"):
+        """``kv``: PagedKVCache-like object with ``latent[l]`` [num_blocks, block_size, 576] bf16
+        per layer, ``block_tables``, ``bm`` (see models.deepseek.LatentCache)."""
+        self.cfg, self.w, self.kv, self.dev = cfg, w, kv, torch.device(device)
+        self.max_rows = R = min(max_rows, 8)
+        dev = self.dev
+        H, nh = cfg.hidden, cfg.n_heads
+        nope, rd, vd = cfg.qk_nope_dim, cfg.qk_rope_dim, cfg.v_head_dim
+        E, k = max(cfg.n_experts, 1), max(cfg.top_k, 1)
+        F, Fs = max(cfg.expert_ffn, 32), max(cfg.shared_ffn, 32)
+        from .llama import StepInputs
+        self.inp = StepInputs(R, dev)
+        self.x = torch.zeros(R, H, device=dev)
+        self.xa = Q8Act(R, H, dev)
+        self.qa = torch.zeros(R, cfg.q_lora_rank, device=dev)
+        self.qaq = Q8Act(R, cfg.q_lora_rank, dev)
+        self.q = torch.zeros(R, nh * (nope + rd), device=dev)
+        self.kva = torch.zeros(R, LAT + ROPE, device=dev)
+        self.q_lat = torch.zeros(R, nh, LAT, device=dev)
+        self.q_pe = torch.zeros(R, nh, ROPE, device=dev)
+        self.o_lat = torch.zeros(R, nh, LAT, device=dev)
+        self.attq = Q8Act(R, nh * vd, dev)
+        self.h = Q8Act(R, max(cfg.ffn, 32), dev)
+        self.rlog = torch.zeros(R, E, device=dev)
+        self.ids = torch.zeros(R, k, dtype=torch.int32, device=dev)
+        self.rw = torch.zeros(R, k, device=dev)
+        self.counts = torch.zeros(E, dtype=torch.int32, device=dev)
+        self.offsets = torch.zeros(E, dtype=torch.int32, device=dev)
+        self.sorted = torch.zeros(R * k, dtype=torch.int32, device=dev)
+        self.active = torch.zeros(E, dtype=torch.int32, device=dev)
+        self.n_active = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.gx = Q8Act(R * k, H, dev)
+        self.hx = Q8Act(R * k, F, dev)
+        self.hs = Q8Act(R, Fs, dev)
+        self.logits = torch.zeros(R, cfg.vocab, device=dev)
+        self.next_ids = torch.zeros(R, dtype=torch.int32, device=dev)
+        self.rope = ops.rope_table(cfg.max_ctx, ROPE, cfg.rope_theta, None, dev)
+        self.scale = 1.0 / math.sqrt(nope + rd)
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._graphs = {}
+        self.launches_per_graph = 0
+
+    def num_splits(self, rows: int) -> int:
+        s = 1
+        while s < 8 and rows * (self.cfg.n_heads // 4) * s < 148:
+            s *= 2
+        return s
+
+    def _attention(self, l, L, rows):
+        cfg, t, kv, inp = self.cfg, self.w.table, self.kv, self.inp
+        K = kernels()
+        xa = self.xa.view(rows)
+        mixed_gemv(t, L.idx["qa"], xa, self.qa[:rows])
+        ops.rmsnorm_q8(self.qa[:rows], L.q_a_norm, cfg.eps, self.qaq.view(rows))
+        mixed_gemv(t, L.idx["qb"], self.qaq.view(rows), self.q[:rows])
+        mixed_gemv(t, L.idx["kva"], xa, self.kva[:rows])
+        ops.launches.add(4)
+        K.mla_kv_append(self.kva[:rows], L.kv_a_norm, cfg.eps, inp.positions[:rows], kv.block_tables,
+                        inp.row_seq[:rows], self.rope, kv.latent[l], ops.PDL)
+        K.mla_absorb_q(self.q[:rows], L.w_uk, inp.positions[:rows], self.rope, self.q_lat[:rows], self.q_pe[:rows],
+                       ops.PDL)
+        K.mla_decode(self.q_lat[:rows], self.q_pe[:rows], kv.latent[l], kv.block_tables, inp.row_seq[:rows],
+                     inp.row_ctx[:rows], self.scale, self.num_splits(rows), self.o_lat[:rows], self.status, ops.PDL)
+        K.mla_out(self.o_lat[:rows], L.w_uv, self.attq.q[:rows], self.attq.d[:rows], self.attq.s[:rows], ops.PDL)
+        mixed_gemv(t, L.idx["o"], self.attq.view(rows), self.x[:rows], residual=True)
+
+    def _ffn(self, L, rows):
+        cfg, t = self.cfg, self.w.table
+        xa = self.xa.view(rows)
+        if L.dense:
+            h = self.h.view(rows)
+            mixed_gemv_swiglu(t, L.idx["g"], L.idx["u"], xa, h)
+            mixed_gemv(t, L.idx["d"], h, self.x[:rows], residual=True)
+            return
+        E, k, H, F = cfg.n_experts, cfg.top_k, cfg.hidden, cfg.expert_ffn
+        ops.router_logits(L.router, xa, self.rlog[:rows])
+        ops.moe_topk(self.rlog[:rows], L.router_bias, k, 1, cfg.n_groups, cfg.topk_groups, cfg.norm_topk,
+                     cfg.routed_scale, self.ids[:rows], self.rw[:rows])
+        ops.moe_align(self.ids[:rows], E, xa, self.counts, self.offsets, self.sorted, self.gx)
+        K = kernels()
+        ops.launches.add(3)
+        K.moe_active(self.counts, self.active, self.n_active, ops.PDL)
+        na = min(E, rows * k)
+        K.moe_mixed_gemv(0, t.descs, L.idx["eg"], L.idx["eu"], F, H, k, self.counts, self.offsets, self.sorted,
+                         self.active, self.n_active, na, self.gx.q, self.gx.d, self.gx.s, self.hx.q, self.hx.d,
+                         self.hx.s, None, None, ops.PDL)
+        K.moe_mixed_gemv(1, t.descs, L.idx["ed"], L.idx["ed"], H, F, k, self.counts, self.offsets, self.sorted,
+                         self.active, self.n_active, na, self.hx.q, self.hx.d, self.hx.s, None, None, None,
+                         self.x[:rows], self.rw[:rows].reshape(-1), ops.PDL)
+        hs = self.hs.view(rows)
+        mixed_gemv_swiglu(t, L.idx["sg"], L.idx["su"], xa, hs)
+        mixed_gemv(t, L.idx["sd"], hs, self.x[:rows], residual=True)
+
+    def forward(self, rows: int, sample: str = "greedy", advance: bool = False):
+        cfg, w, inp = self.cfg, self.w, self.inp
+        ops.embed(w.embed, inp.ids[:rows], self.x[:rows])
+        for l, L in enumerate(w.layers):
+            ops.rmsnorm_q8(self.x[:rows], L.attn_norm, cfg.eps, self.xa.view(rows))
+            self._attention(l, L, rows)
+            ops.rmsnorm_q8(self.x[:rows], L.ffn_norm, cfg.eps, self.xa.view(rows))
+            self._ffn(L, rows)
+        ops.rmsnorm_q8(self.x[:rows], w.out_norm, cfg.eps, self.xa.view(rows))
+        mixed_gemv(w.table, w.lm_head, self.xa.view(rows), self.logits[:rows])
+        if sample == "greedy":
+            ops.argmax(self.logits[:rows], self.next_ids[:rows])
+        if advance:
+            ops.advance(inp.ids, self.next_ids, inp.positions, inp.row_ctx, rows)
+
+    def forward_tokens(self, tokens, seq_id: int = 0, start_pos: int = 0) -> torch.Tensor:
+        """Teacher-forced forward of one sequence in chunks of up to 8 rows; fp32 logits [n, vocab]."""
+        kv = self.kv
+        n = len(tokens)
+        if not kv.bm.reserve(seq_id, start_pos + n):
+            raise RuntimeError("latent cache exhausted")
+        kv.sync_tables([seq_id])
+        r = kv.row(seq_id)
+        out = torch.empty(n, self.cfg.vocab, device=self.dev)
+        for c0 in range(0, n, self.max_rows):
+            c1 = min(n, c0 + self.max_rows)
+            pos = list(range(start_pos + c0, start_pos + c1))
+            self.inp.upload(tokens[c0:c1], pos, [0] * (c1 - c0), [r] * (c1 - c0), [p + 1 for p in pos])
+            self.forward(c1 - c0, "greedy")
+            out[c0:c1] = self.logits[: c1 - c0]
+        return out
+
+    def graph_forward(self, rows: int, sample: str = "greedy", advance: bool = False):
+        key = (rows, sample, advance)
+        g = self._graphs.get(key)
+        if g is None:
+            s = torch.cuda.Stream(self.dev)
+            s.wait_stream(torch.cuda.current_stream(self.dev))
+            with torch.cuda.stream(s):
+                self.forward(rows, "none")
+            torch.cuda.current_stream(self.dev).wait_stream(s)
+            g = torch.cuda.CUDAGraph()
+            n0 = ops.launches.n
+            with torch.cuda.graph(g):
+                self.forward(rows, sample, advance)
+            self.launches_per_graph = ops.launches.n - n0
+            self._graphs[key] = g
+        g.replay()
+
+
+class LatentCache:
+    """Paged latent cache: ``latent[l]`` [num_blocks, block_size, 576] bf16 per layer, with the
+    C++ block manager and device block tables of the regular paged KV cache."""
+
+    def __init__(self, layers: int, num_blocks: int, block_size: int, max_seqs: int, max_blocks: int, device):
+        from ..engine.kv_cache import PagedKVCache
+        self._kv = PagedKVCache(1, 1, 64, num_blocks, block_size, max_seqs, max_blocks, device)
+        self.latent = [torch.zeros(num_blocks, block_size, LAT + ROPE, dtype=torch.bfloat16, device=device)
+                       for _ in range(layers)]
+        self.block_size = block_size
+        self.bm = self._kv.bm
+        self.block_tables = self._kv.block_tables
+
+    def sync_tables(self, ids):
+        self._kv.sync_tables(ids)
+
+    def row(self, seq_id):
+        return self._kv.row(seq_id)
+
+    def drop(self, seq_id):
+        self._kv.drop(seq_id)
+
+
+# ---- fp32 PyTorch reference (test oracle) -----------------------------------------------------
+class TorchRefDeepSeek:
+    """Token-serial fp32 restatement with the un-absorbed MLA (keys and values reconstructed from
+    the latent per head, as in the reference CPU oracle) and the device's activation rounding."""
+
+    def __init__(self, cfg: ModelConfig, w: DSWeights, act_q8: bool = True):
+        self.cfg, self.w, self.act_q8 = cfg, w, act_q8
+        self.W = [mw.dequantize() for mw in w.table.weights]
+        self.E = w.embed.dequantize()
+        self.cache = {l: [] for l in range(cfg.layers)}
+
+    def _q(self, v):
+        if not self.act_q8:
+            return v
+        b = v.reshape(-1, 32)
+        d = b.abs().amax(1, keepdim=True) / 127.0
+        q = torch.where(d > 0, torch.round(b / torch.where(d > 0, d, torch.ones_like(d))), torch.zeros_like(b))
+        return (q * d).reshape(v.shape)
+
+    @staticmethod
+    def _rms(x, w, eps):
+        return x * torch.rsqrt((x * x).mean() + eps) * w
+
+    def _rope(self, x, pos):
+        inv = 1.0 / (self.cfg.rope_theta ** (torch.arange(0, ROPE, 2, device=x.device, dtype=torch.float64) / ROPE))
+        ang = (pos * inv).float()
+        c, s = torch.cos(ang), torch.sin(ang)
+        a, b = x[..., :ROPE // 2], x[..., ROPE // 2:]
+        return torch.cat([a * c - b * s, b * c + a * s], -1)
+
+    def _route(self, L, h):
+        cfg = self.cfg
+        logits = L.router @ h
+        s = torch.sigmoid(logits)
+        choice = s + L.router_bias
+        E, ng = cfg.n_experts, cfg.n_groups
+        gs = choice.view(ng, E // ng).topk(2, dim=1).values.sum(1)
+        keep = torch.zeros(ng, dtype=torch.bool, device=h.device)
+        keep[gs.topk(cfg.topk_groups).indices] = True
+        masked = torch.where(keep.repeat_interleave(E // ng), choice, torch.full_like(choice, -float("inf")))
+        idx = masked.topk(cfg.top_k).indices
+        wts = s[idx]
+        if cfg.norm_topk:
+            wts = wts / wts.sum()
+        return idx.tolist(), wts * cfg.routed_scale
+
+    def step(self, token: int, pos: int) -> torch.Tensor:
+        cfg, w, W = self.cfg, self.w, self.W
+        nh, nope, rd, vd = cfg.n_heads, cfg.qk_nope_dim, cfg.qk_rope_dim, cfg.v_head_dim
+        x = self.E[token].clone()
+        for l, L in enumerate(w.layers):
+            h = self._q(self._rms(x, L.attn_norm, cfg.eps))
+            qa = W[L.idx["qa"]] @ h
+            q = (W[L.idx["qb"]] @ self._q(self._rms(qa, L.q_a_norm, cfg.eps))).view(nh, nope + rd)
+            kva = W[L.idx["kva"]] @ h
+            c = self._rms(kva[:LAT], L.kv_a_norm, cfg.eps).bfloat16().float()
+            kpe = self._rope(kva[LAT:], pos).bfloat16().float()
+            self.cache[l].append((c, kpe))
+            C = torch.stack([a for a, _ in self.cache[l]])      # [T, 512]
+            KP = torch.stack([b for _, b in self.cache[l]])     # [T, 64]
+            o = torch.empty(nh, vd, device=x.device)
+            uk, uv = L.w_uk.float(), L.w_uv.float()
+            for i in range(nh):
+                k_nope = C @ uk[i].t()                          # [T, nope]
+                v = C @ uv[i].t()                               # [T, vd]
+                qpe = self._rope(q[i, nope:], pos)
+                sc = (k_nope @ q[i, :nope] + KP @ qpe) / math.sqrt(nope + rd)
+                o[i] = torch.softmax(sc, 0) @ v
+            x = x + W[L.idx["o"]] @ self._q(o.reshape(-1))
+            h = self._q(self._rms(x, L.ffn_norm, cfg.eps))
+            if L.dense:
+                gt, up = W[L.idx["g"]] @ h, W[L.idx["u"]] @ h
+                x = x + W[L.idx["d"]] @ self._q(gt / (1 + torch.exp(-gt)) * up)
+            else:
+                idx, wts = self._route(L, h)
+                for e, wt in zip(idx, wts):
+                    gt, up = W[L.idx["eg"] + e] @ h, W[L.idx["eu"] + e] @ h
+                    x = x + wt * (W[L.idx["ed"] + e] @ self._q(gt / (1 + torch.exp(-gt)) * up))
+                gt, up = W[L.idx["sg"]] @ h, W[L.idx["su"]] @ h
+                x = x + W[L.idx["sd"]] @ self._q(gt / (1 + torch.exp(-gt)) * up)
+        h = self._q(self._rms(x, w.out_norm, cfg.eps))
+        return W[w.lm_head] @ h

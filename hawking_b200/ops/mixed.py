@@ -19,7 +19,7 @@ import torch
 
 from .._ext import kernels
 
-BINARY, UNIFORM = 0, 1
+BINARY, UNIFORM, FP8 = 0, 1, 2
 
 
 def _pack_lsb(codes: torch.Tensor, bits: int) -> torch.Tensor:
@@ -50,11 +50,11 @@ class MixedWeight:
 
     @property
     def bound(self) -> int:
-        return 0 if self.kind == BINARY else (1 << (self.bits - 1)) - 1
+        return (1 << (self.bits - 1)) - 1 if self.kind == UNIFORM else 0
 
     @property
     def nbytes(self) -> int:
-        return self.codes.numel() + self.scales.numel() * 2
+        return self.codes.numel() + self.scales.numel() * self.scales.element_size()
 
     @property
     def bpw(self) -> float:
@@ -78,6 +78,36 @@ class MixedWeight:
             codes = (torch.round(g * inv.unsqueeze(-1)).clamp(-bound, bound) + bound).reshape(N, K).to(torch.uint8)
         return MixedWeight(kind, bits, group, N, K, _pack_lsb(codes, bits).contiguous(),
                            scale.to(torch.float16).contiguous())
+
+    @staticmethod
+    def quantize_fp8(w: torch.Tensor, block: int = 128) -> "MixedWeight":
+        """fp8 e4m3 with one fp32 scale per block x block tile (scale = amax / 448), the scale of a
+        row's tile stored per row ([N, K / block])."""
+        N, K = w.shape
+        nbr, nbc = -(-N // block), K // block
+        wp = torch.zeros(nbr * block, K, device=w.device)
+        wp[:N] = w.float()
+        tiles = wp.view(nbr, block, nbc, block)
+        sc = tiles.abs().amax(dim=(1, 3)) / 448.0
+        sc = torch.where(sc > 0, sc, torch.ones_like(sc))
+        q = (tiles / sc[:, None, :, None]).view(nbr * block, K)[:N].to(torch.float8_e4m3fn)
+        scales = sc.repeat_interleave(block, 0)[:N].contiguous()
+        return MixedWeight(FP8, 8, block, N, K, q.view(torch.uint8).contiguous(), scales)
+
+    @staticmethod
+    def random_fp8(N: int, K: int, std: float, gen: torch.Generator, device, block: int = 128,
+                   chunk_rows: int = 8192) -> "MixedWeight":
+        """Random-init N(0, std) weights in fp8 e4m3 with 128 x 128 block scales, generated in row
+        chunks (benchmark weights)."""
+        codes = torch.empty(N, K, dtype=torch.uint8, device=device)
+        nbc = K // block
+        scales = torch.empty(N, nbc, dtype=torch.float32, device=device)
+        for r0 in range(0, N, chunk_rows):
+            r1 = min(N, r0 + chunk_rows)
+            part = MixedWeight.quantize_fp8(torch.randn(r1 - r0, K, generator=gen, device=device) * std, block)
+            codes[r0:r1] = part.codes
+            scales[r0:r1] = part.scales
+        return MixedWeight(FP8, 8, block, N, K, codes, scales)
 
     @staticmethod
     def random(N: int, K: int, kind: int, bits: int, group: int, std: float, gen: torch.Generator, device) -> "MixedWeight":
@@ -116,6 +146,8 @@ class MixedWeight:
         return MixedWeight(kind, bits, gs, rows, cols, codes.to(device).contiguous(), scales.to(device).contiguous())
 
     def dequantize(self) -> torch.Tensor:
+        if self.kind == FP8:
+            return self.codes.view(torch.float8_e4m3fn).float() * self.scales.repeat_interleave(self.group, 1)
         c = _unpack_lsb(self.codes, self.bits, self.K).float()
         s = self.scales.float().repeat_interleave(self.group, 1)
         if self.kind == BINARY:
