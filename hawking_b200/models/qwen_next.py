@@ -78,7 +78,7 @@ def expert_codec(rng: random.Random, ternary_fraction: float):
 
 
 def random_qwen_next_weights(cfg: ModelConfig, device, seed: int = 0, std: float = 0.02,
-                             ternary_fraction: float = 0.12, group: int = 64, materialise: bool = False) -> QNWeights:
+                             ternary_fraction: float = 0.10, group: int = 64, materialise: bool = False) -> QNWeights:
     """Random-init weights in the benchmark's mixed recipe. ``materialise`` draws Gaussian weights
     and encodes them (small configs / tests); otherwise random codes and Gaussian-statistics
     scales are written directly (the 80B benchmark model)."""
