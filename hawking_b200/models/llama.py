@@ -398,8 +398,6 @@ class LlamaModel:
             raise NotImplementedError("tensor-parallel sampling: greedy only")
         if n_logits < 0:
             return
-        if nl > GEMV_COLS:
-            raise RuntimeError("tensor-parallel LM head takes at most 8 rows")
         if tc or n_logits:
             # the residual is in self.x; normalise the sampled rows here
             src = self.x[:rows]
@@ -408,10 +406,11 @@ class LlamaModel:
             ops.rmsnorm_q8(src, w.out_norm, cfg.eps, self.xa.view(nl))
         # else: the last layer's all-reduce left norm(x) in self.xa
         if sample == "none":  # this rank's vocabulary slice of the logits only
-            ops.gemv(w.lm_head, self.xa_view(0, nl), self.logits[:nl])
+            self._gemv_cols(lambda c0, c1: ops.gemv(w.lm_head, self.xa_view(c0, c1), self.logits[c0:c1]), nl)
             return
-        ops.gemv(w.lm_head, self.xa_view(0, nl), self.logits[:nl], argmax_slots=self.argmax_slots[:nl],
-                 argmax_offset=tp.rank * w.lm_head.N)
+        self._gemv_cols(lambda c0, c1: ops.gemv(w.lm_head, self.xa_view(c0, c1), self.logits[c0:c1],
+                                                argmax_slots=self.argmax_slots[c0:c1],
+                                                argmax_offset=tp.rank * w.lm_head.N), nl)
         ops.tp_argmax(tp, self.argmax_slots, nl, self.next_ids)
 
     def _attention_block_tc(self, l, lw, rows, splits):

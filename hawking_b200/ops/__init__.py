@@ -100,7 +100,9 @@ def tp_argmax(tp, slots: torch.Tensor, rows: int, out: torch.Tensor):
     """Global greedy ids from every rank's fused LM-head keys (vocabulary-parallel)."""
     launches.add()
     site = tp.argmax_site
-    kernels().tp_argmax(slots, rows, tp.max_rows, tp.keys_table, tp.base + tp.keys_off, tp.push_counters[site],
+    if rows > tp.key_rows:
+        raise ValueError(f"tp_argmax: {rows} rows exceed the key region ({tp.key_rows})")
+    kernels().tp_argmax(slots, rows, tp.key_rows, tp.keys_table, tp.base + tp.keys_off, tp.push_counters[site],
                         tp.counter_local(site), tp.argmax_uses, tp.rank, out, tp.status, PDL)
 
 

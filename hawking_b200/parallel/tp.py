@@ -118,17 +118,19 @@ class TPComm:
     """Shared buffers and pointer tables of the fused collectives for one rank."""
 
     def __init__(self, rank: int, world: int, n_sites: int, max_rows: int, width: int, device,
-                 group: Optional[dist.ProcessGroup] = None):
+                 group: Optional[dist.ProcessGroup] = None, key_rows: int = 64):
+        """``max_rows``: rows of the push all-reduce (GEMV path); ``key_rows``: rows of the greedy
+        key exchange (any decode batch)."""
         K = kernels()
         self.rank, self.world, self.n_sites = rank, world, n_sites
-        self.max_rows, self.width = max_rows, width
+        self.max_rows, self.width, self.key_rows = max_rows, width, key_rows
         self.dev = torch.device(device)
         self.group = group
         self.rank_stride = max_rows * width                       # floats per source rank
         self.site_floats = world * self.rank_stride
         recv_bytes = n_sites * self.site_floats * 4
         self.keys_off = recv_bytes
-        keys_bytes = world * max_rows * 8
+        keys_bytes = world * key_rows * 8
         self.cnt_off = self.keys_off + keys_bytes
         total = self.cnt_off + (n_sites + 1) * 8
         total = (total + 255) // 256 * 256
