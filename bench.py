@@ -47,6 +47,12 @@ def parse():
     ap.add_argument("--profile-step", action="store_true",
                     help="run one eager decode step between cudaProfilerStart/Stop (for ncu --profile-from-start off) "
                          "and exit without a result line")
+    ap.add_argument("--tp-shard-of", type=int, default=0,
+                    help="one GPU runs rank 0's shard of an N-way tensor-parallel model with its collectives looped "
+                         "back to itself (profiling the shard's kernels under a single-process profiler; not a result)")
+    ap.add_argument("--profile-prefill", action="store_true",
+                    help="run one --ctx-token prompt prefill through the engine between cudaProfilerStart/Stop "
+                         "(after one untimed prefill) and exit without a result line")
     return ap.parse_args()
 
 
@@ -256,11 +262,12 @@ def main():
     use_tp = world > 1 and args.parallel == "tp"
     t0 = time.time()
     tp = None
-    if use_tp:
+    if use_tp or args.tp_shard_of > 1:
         from hawking_b200.parallel.tp import TPComm, local_config, random_llama_weights_tp
-        w = random_llama_weights_tp(cfg, rank, world, dev, seed=0)
+        shards = args.tp_shard_of if world == 1 else world
+        w = random_llama_weights_tp(cfg, rank, shards, dev, seed=0)
         tp = TPComm(rank, world, 2 * cfg.layers, 8, cfg.hidden, dev)
-        mcfg = local_config(cfg, world)
+        mcfg = local_config(cfg, shards)
     else:
         w = random_llama_weights(cfg, dev, seed=0)
         mcfg = cfg
@@ -318,6 +325,20 @@ def main():
     for l in range(cfg.layers):
         kv.k[l].normal_(0, 1, generator=g)
         kv.v[l].normal_(0, 1, generator=g)
+
+    if args.profile_prefill:
+        for run in range(2):
+            prompt = random_prompt(ctx, cfg.vocab, seed=100 + run)
+            torch.cuda.synchronize()
+            if run:
+                torch.cuda.cudart().cudaProfilerStart()
+            rid = eng.add_request(prompt, SamplingParams(max_tokens=1))
+            while eng.has_work():
+                eng.step()
+            torch.cuda.synchronize()
+        torch.cuda.cudart().cudaProfilerStop()
+        print(json.dumps({"profile_prefill": True, "prompt": ctx}))
+        return 0
 
     # ---- bs1 (or --batch) device-timed decode ----
     seqs = setup_decode(B, 1_000_000)
@@ -416,6 +437,8 @@ def main():
         "weight_bw_gbs": round(w.nbytes / (ms1 * 1e-3) / 1e9, 1),
         "load_s": round(t_load, 1),
     }
+    if args.tp_shard_of > 1 and world == 1:
+        out["invalid"] = f"one GPU ran rank 0's shard of a {args.tp_shard_of}-way TP model, collectives looped back"
     if tp is not None:
         tp.check()
         out["tp_collectives"] = "decode: GEMV epilogue pushes partials over NVLink + fused all-reduce/RMSNorm; " \

@@ -41,7 +41,7 @@ void gemv(int64_t fmt, int64_t epi, const std::vector<Tensor>& w0, const std::ve
           const optional<Tensor>& y, const optional<Tensor>& bias, const optional<Tensor>& oq,
           const optional<Tensor>& od, const optional<Tensor>& os, const optional<Tensor>& x_f32,
           const optional<Tensor>& norm_w, double eps, bool pdl, const optional<Tensor>& argmax_slots,
-          int64_t argmax_offset, const optional<Tensor>& push_recv, const optional<Tensor>& push_counters) {
+          int64_t argmax_offset, const optional<Tensor>& push_recv, const optional<Tensor>& push_epoch) {
   hk::GemvArgs a{};
   int nb;
   if (x_f32.has_value()) {
@@ -89,12 +89,12 @@ void gemv(int64_t fmt, int64_t epi, const std::vector<Tensor>& w0, const std::ve
     a.argmax_offset = argmax_offset;
   }
   if (epi == hk::EPI_PUSH) {
-    TORCH_CHECK(push_recv.has_value() && push_counters.has_value(), "gemv push: peer pointer tables required");
-    TORCH_CHECK(push_recv->is_cuda() && push_recv->scalar_type() == at::kLong && push_counters->is_cuda() &&
-                    push_counters->scalar_type() == at::kLong && push_recv->numel() == push_counters->numel(),
-                "gemv push: int64 device pointer tables of equal length");
-    a.push_recv = reinterpret_cast<float* const*>(push_recv->data_ptr<int64_t>());
-    a.push_counters = reinterpret_cast<unsigned long long* const*>(push_counters->data_ptr<int64_t>());
+    TORCH_CHECK(push_recv.has_value() && push_epoch.has_value(), "gemv push: peer pointer table and epoch required");
+    TORCH_CHECK(push_recv->is_cuda() && push_recv->scalar_type() == at::kLong && push_epoch->is_cuda() &&
+                    push_epoch->scalar_type() == at::kInt,
+                "gemv push: int64 device pointer table and int32 epoch");
+    a.push_recv = reinterpret_cast<unsigned long long* const*>(push_recv->data_ptr<int64_t>());
+    a.push_epoch = push_epoch->data_ptr<int>();
     a.push_n = (int)push_recv->numel();
   }
   if (epi == hk::EPI_SWIGLU_Q8) {
@@ -214,6 +214,42 @@ void attention_decode(const Tensor& q, const Tensor& k_cache, const Tensor& v_ca
   else hk::attention_decode_launch(a, cur_stream(), pdl);
 }
 
+void attention_prefill(const Tensor& q, const Tensor& k_cache, const Tensor& v_cache, const Tensor& block_tables,
+                       const Tensor& row_seq, const Tensor& row_ctx, double scale, const optional<Tensor>& out,
+                       const optional<Tensor>& oq, const optional<Tensor>& od, const optional<Tensor>& os,
+                       const optional<Tensor>& sinks, const optional<Tensor>& out_bf16, bool pdl) {
+  check_cuda(q, "q");
+  TORCH_CHECK(q.dim() == 3 && q.scalar_type() == at::kFloat && q.is_contiguous(), "q must be contiguous fp32 [R, nh, hd]");
+  TORCH_CHECK(k_cache.dim() == 4 && k_cache.scalar_type() == at::kBFloat16 && v_cache.sizes() == k_cache.sizes(),
+              "k_cache / v_cache must be bf16 [blocks, nkv, bs, hd]");
+  TORCH_CHECK(block_tables.scalar_type() == at::kInt && row_seq.scalar_type() == at::kInt &&
+                  row_ctx.scalar_type() == at::kInt, "block tables / rows must be int32");
+  hk::AttnDecodeArgs a{};
+  a.q = ptr<float>(q);
+  a.k_cache = ptr<__nv_bfloat16>(k_cache);
+  a.v_cache = ptr<__nv_bfloat16>(v_cache);
+  a.block_tables = ptr<int>(block_tables);
+  a.max_blocks = (int)block_tables.size(1);
+  a.row_seq = ptr<int>(row_seq);
+  a.row_ctx = ptr<int>(row_ctx);
+  a.scale = (float)scale;
+  a.R = (int)q.size(0);
+  a.nh = (int)q.size(1);
+  a.hd = (int)q.size(2);
+  a.nkv = (int)k_cache.size(1);
+  a.block_size = (int)k_cache.size(2);
+  TORCH_CHECK(k_cache.size(3) == a.hd, "attention prefill: head_dim mismatch");
+  a.out = optr<float>(out);
+  a.oq = optr<int8_t>(oq);
+  a.od = optr<float>(od);
+  a.os = optr<float>(os);
+  a.sinks = optr<float>(sinks);
+  a.out_bf16 = optr<__nv_bfloat16>(out_bf16);
+  TORCH_CHECK(!a.oq || (a.od && a.os), "attention prefill: q8 output needs d and s");
+  const c10::cuda::CUDAGuard g(q.device());
+  hk::attention_prefill_launch(a, cur_stream(), pdl);
+}
+
 void argmax(const Tensor& logits, const Tensor& out, bool pdl) {
   check_cuda(logits, "logits");
   TORCH_CHECK(logits.scalar_type() == at::kFloat && out.scalar_type() == at::kInt, "argmax: fp32 logits, int32 out");
@@ -260,7 +296,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("oq") = py::none(), py::arg("od") = py::none(), py::arg("os") = py::none(),
         py::arg("x_f32") = py::none(), py::arg("norm_w") = py::none(), py::arg("eps") = -1.0,
         py::arg("pdl") = false, py::arg("argmax_slots") = py::none(), py::arg("argmax_offset") = 0,
-        py::arg("push_recv") = py::none(), py::arg("push_counters") = py::none());
+        py::arg("push_recv") = py::none(), py::arg("push_epoch") = py::none());
   m.def("rmsnorm_q8", &rmsnorm_q8, py::arg("x"), py::arg("w"), py::arg("eps"), py::arg("norm"), py::arg("xq"),
         py::arg("xd"), py::arg("xs"), py::arg("y") = py::none(), py::arg("pdl") = false);
   m.def("rmsnorm", &rmsnorm, py::arg("x"), py::arg("w"), py::arg("eps"), py::arg("yf") = py::none(),
@@ -277,6 +313,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
                        cur_stream(), pdl);
   }, py::arg("ids"), py::arg("next_ids"), py::arg("positions"), py::arg("row_ctx"), py::arg("R"),
         py::arg("pdl") = false);
+  m.def("attention_prefill", &attention_prefill, py::arg("q"), py::arg("k_cache"), py::arg("v_cache"),
+        py::arg("block_tables"), py::arg("row_seq"), py::arg("row_ctx"), py::arg("scale"), py::arg("out"),
+        py::arg("oq"), py::arg("od"), py::arg("os"), py::arg("sinks"), py::arg("out_bf16"), py::arg("pdl") = false);
   m.def("attention_decode", &attention_decode, py::arg("q"), py::arg("k_cache"), py::arg("v_cache"),
         py::arg("block_tables"), py::arg("row_seq"), py::arg("row_ctx"), py::arg("scale"), py::arg("num_splits"),
         py::arg("part_o"), py::arg("part_lse"), py::arg("out") = py::none(), py::arg("oq") = py::none(),

@@ -57,7 +57,7 @@ void tp_begin(const Tensor& epoch, bool pdl) {
 }
 
 void tp_allreduce_rmsnorm_q8(const Tensor& x_in, const Tensor& x_out, int64_t recv, int64_t rank_stride, int64_t n,
-                             int64_t counter, const Tensor& epoch, int64_t producer_ctas, const c10::optional<Tensor>& w,
+                             const Tensor& epoch, const c10::optional<Tensor>& w,
                              double eps, const Tensor& xq, const Tensor& xd, const Tensor& xs, const Tensor& status,
                              bool pdl) {
   TORCH_CHECK(x_in.is_cuda() && x_in.scalar_type() == at::kFloat && x_out.scalar_type() == at::kFloat,
@@ -67,12 +67,10 @@ void tp_allreduce_rmsnorm_q8(const Tensor& x_in, const Tensor& x_out, int64_t re
   a.x_in = x_in.data_ptr<float>();
   a.x_out = x_out.data_ptr<float>();
   a.x_stride = x_in.stride(0);
-  a.recv = as_ptr<const float>(recv);
+  a.recv = as_ptr<const unsigned long long>(recv);
   a.rank_stride = rank_stride;
   a.n = (int)n;
-  a.counter = as_ptr<const unsigned long long>(counter);
   a.epoch = epoch.data_ptr<int>();
-  a.producer_ctas = (int)producer_ctas;
   a.w = w.has_value() ? w->data_ptr<float>() : nullptr;
   a.eps = (float)eps;
   a.K = (int)x_in.size(1);
@@ -85,20 +83,17 @@ void tp_allreduce_rmsnorm_q8(const Tensor& x_in, const Tensor& x_out, int64_t re
 }
 
 void tp_argmax(const Tensor& slots, int64_t rows, int64_t max_rows, const Tensor& keys_table, int64_t keys_local,
-               const Tensor& counters_table, int64_t counter_local, const Tensor& epoch, int64_t me, const Tensor& out,
-               const Tensor& status, bool pdl) {
+               const Tensor& uses, int64_t me, const Tensor& out, const Tensor& status, bool pdl) {
   TORCH_CHECK(slots.is_cuda() && slots.scalar_type() == at::kLong, "tp_argmax: int64 slots");
-  TORCH_CHECK(keys_table.scalar_type() == at::kLong && counters_table.scalar_type() == at::kLong &&
-                  keys_table.numel() == counters_table.numel(), "tp_argmax: int64 pointer tables");
+  TORCH_CHECK(keys_table.scalar_type() == at::kLong, "tp_argmax: int64 pointer table");
+  TORCH_CHECK(rows <= max_rows, "tp_argmax: rows exceed the key region");
   hk::TpArgmaxArgs a{};
   a.slots = reinterpret_cast<unsigned long long*>(slots.data_ptr<int64_t>());
   a.rows = (int)rows;
   a.max_rows = (int)max_rows;
   a.keys = reinterpret_cast<unsigned long long* const*>(keys_table.data_ptr<int64_t>());
   a.keys_local = as_ptr<const unsigned long long>(keys_local);
-  a.counters = reinterpret_cast<unsigned long long* const*>(counters_table.data_ptr<int64_t>());
-  a.counter_local = as_ptr<const unsigned long long>(counter_local);
-  a.uses = epoch.data_ptr<int>();
+  a.uses = uses.data_ptr<int>();
   a.me = (int)me;
   a.n = (int)keys_table.numel();
   a.out = out.data_ptr<int>();
@@ -117,11 +112,9 @@ void register_tp_kernels(py::module_& m) {
   m.def("ipc_free", &ipc_free, py::arg("ptr"));
   m.def("tp_begin", &tp_begin, py::arg("epoch"), py::arg("pdl") = false);
   m.def("tp_allreduce_rmsnorm_q8", &tp_allreduce_rmsnorm_q8, py::arg("x_in"), py::arg("x_out"), py::arg("recv"),
-        py::arg("rank_stride"), py::arg("n"), py::arg("counter"), py::arg("epoch"), py::arg("producer_ctas"),
-        py::arg("w"), py::arg("eps"), py::arg("xq"), py::arg("xd"), py::arg("xs"), py::arg("status"),
+        py::arg("rank_stride"), py::arg("n"), py::arg("epoch"), py::arg("w"), py::arg("eps"), py::arg("xq"), py::arg("xd"), py::arg("xs"), py::arg("status"),
         py::arg("pdl") = false);
   m.def("tp_argmax", &tp_argmax, py::arg("slots"), py::arg("rows"), py::arg("max_rows"), py::arg("keys_table"),
-        py::arg("keys_local"), py::arg("counters_table"), py::arg("counter_local"), py::arg("epoch"), py::arg("me"),
-        py::arg("out"), py::arg("status"), py::arg("pdl") = false);
+        py::arg("keys_local"), py::arg("uses"), py::arg("me"), py::arg("out"), py::arg("status"), py::arg("pdl") = false);
 }
 }  // namespace hk

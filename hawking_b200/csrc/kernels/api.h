@@ -58,28 +58,22 @@ struct GemvArgs {
   unsigned long long* argmax_slots;
   int64_t argmax_offset;   // added to row indices in the packed keys (vocabulary-parallel LM head)
   // EPI_PUSH (tensor-parallel row-parallel projection): every output (row, column b) is stored to
-  // push_recv[p][b * N + row] on every rank p, then each CTA arrives once on push_counters[p].
-  float* const* push_recv;
-  unsigned long long* const* push_counters;
+  // push_recv[p][b * N + row] on every rank p as one flagged word (value | step epoch << 32).
+  unsigned long long* const* push_recv;
+  const int* push_epoch;
   int push_n;
 };
 constexpr int kArgmaxSlots = 256;
 
 // ---- tensor parallel (tp.cu) ----
-struct TpSite {
-  unsigned long long* const* counters;  // [n] device pointers to every rank's counter of this site
-  int me, n;
-};
 struct TpReduceArgs {
   const float* x_in;            // residual before the projection [rows, x_stride]
   float* x_out;                 // residual after it (a different buffer)
   int64_t x_stride;
-  const float* recv;            // this rank's receive region of the site: [n][rows][K] partials
-  int64_t rank_stride;          // floats between source ranks in `recv`
+  const unsigned long long* recv;  // this rank's receive region of the site: [n][rows][K] flagged words
+  int64_t rank_stride;          // words between source ranks in `recv`
   int n;
-  const unsigned long long* counter;  // this rank's arrival counter of the site
-  const int* epoch;
-  int producer_ctas;            // CTAs per rank that arrive on the counter each step
+  const int* epoch;             // flag of this step's words
   const float* w;               // RMSNorm weight of the next projection
   float eps;
   int K;
@@ -91,11 +85,9 @@ struct TpReduceArgs {
 struct TpArgmaxArgs {
   unsigned long long* slots;    // local fused-argmax slots [rows, kArgmaxSlots] (cleared here)
   int rows, max_rows;
-  unsigned long long* const* keys;       // [n] device pointers: every rank's key region [n][max_rows]
+  unsigned long long* const* keys;       // [n] every rank's key region [n][max_rows][2] flagged words
   const unsigned long long* keys_local;  // this rank's key region
-  unsigned long long* const* counters;   // [n] device pointers to every rank's counter of the site
-  const unsigned long long* counter_local;
-  int* uses;                    // this rank's count of argmax rounds (device, updated here)
+  int* uses;                    // this rank's count of argmax rounds = the flag (device, updated here)
   int me, n;
   int* out;                     // token ids [rows]
   int* status;
@@ -164,6 +156,9 @@ void attention_decode_launch(const AttnDecodeArgs& a, cudaStream_t s, bool pdl);
 // Cluster variant (num_splits in {1, 2, 4, 8}): the splits of one (row, kv head) merge through
 // distributed shared memory; part_o / part_lse / counters are not used.
 void attention_decode_cluster_launch(const AttnDecodeArgs& a, cudaStream_t s, bool pdl);
+// Causal prefill on the tensor cores (attention_prefill.cu): any rows (runs of one sequence are
+// found on the device), head_dim 64 or 128; outputs out / out_bf16 / q8 (split fields unused).
+void attention_prefill_launch(const AttnDecodeArgs& a, cudaStream_t s, bool pdl);
 
 // Reduce the packed argmax slots of `rows` batch columns to token ids and zero the slots.
 void argmax_finalize_launch(unsigned long long* slots, int rows, int* out, cudaStream_t s, bool pdl);

@@ -284,9 +284,9 @@ __global__ void __launch_bounds__(256, (NB == 1 && XIN == XIN_Q8) ? (EPI == EPI_
       for (int c = 1; c < NB; ++c)
         if (lane == c) v = acc[c];
       if (a.bias) v += a.bias[row];
-      for (int p = 0; p < a.push_n; ++p) a.push_recv[p][(int64_t)lane * a.N + row] = v;
+      const uint32_t flag = (uint32_t)*a.push_epoch;
+      for (int p = 0; p < a.push_n; ++p) ll_store(a.push_recv[p] + (int64_t)lane * a.N + row, __float_as_uint(v), flag);
     }
-    tp_signal(TpSite{a.push_counters, 0, a.push_n});
   } else {
     if (!live) { pdl_launch(); return; }
     float acc[NB];
@@ -359,7 +359,7 @@ void gemv_launch(int fmt, int epi, const GemvArgs& a, int nb, cudaStream_t s, bo
     case EPI_STORE: dispatch_fmt<EPI_STORE, XIN_Q8>(fmt, a, nb, s, pdl); break;
     case EPI_RESID: dispatch_fmt<EPI_RESID, XIN_Q8>(fmt, a, nb, s, pdl); break;
     case EPI_PUSH:
-      if (!a.push_recv || !a.push_counters || a.push_n <= 0) throw std::runtime_error("gemv push: peer tables required");
+      if (!a.push_recv || !a.push_epoch || a.push_n <= 0) throw std::runtime_error("gemv push: peer tables required");
       dispatch_fmt<EPI_PUSH, XIN_Q8>(fmt, a, nb, s, pdl);
       break;
     case EPI_SWIGLU_Q8: dispatch_fmt<EPI_SWIGLU_Q8, XIN_Q8>(fmt, a, nb, s, pdl); break;

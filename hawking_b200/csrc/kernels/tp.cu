@@ -2,44 +2,35 @@
 //
 // All-reduce of a row-parallel projection (attention output, FFN down) at decode batch sizes is
 // a one-shot push: the projection GEMV's epilogue stores each of its output rows straight into
-// every rank's receive region (peer pointers from CUDA IPC), then each CTA bumps every rank's
-// arrival counter once with a system-scope release. The next kernel on every rank, the RMSNorm
-// that feeds the following projection, waits (bounded) until all producer CTAs of all ranks have
-// arrived, sums the N partial vectors into the new residual (a second buffer, so no CTA reads
-// what another CTA writes), normalises and quantises. No separate all-reduce launch, no host
-// round trip, no staging copy: the partials cross NVLink once, from the producing SMs.
+// every rank's receive region (peer pointers from CUDA IPC) as flagged words (tp.cuh). The next
+// kernel on every rank, the RMSNorm that feeds the following projection, polls the words of the
+// elements it owns until their flag is this step's epoch (bounded), sums the N partials into the
+// new residual (a second buffer, so no CTA reads what another CTA writes), normalises and
+// quantises. The CTAs of one row form a cluster that adds up the row's sum of squares through
+// distributed shared memory. No separate all-reduce launch, no fence, no counter, no host round
+// trip: the partials cross NVLink once, from the producing SMs.
 //
-// Arrival counters never reset: every rank bumps an epoch at the start of each forward that uses
-// the push sites (the tensor-core prefill path all-reduces with NCCL and does not),
-// and a consumer waits for epoch * (producer CTAs) * N arrivals. A rank cannot overwrite a
+// Every rank bumps the epoch at the start of each forward that uses the push sites (the
+// tensor-core prefill path all-reduces with NCCL and does not). A rank cannot overwrite a
 // receive region that a slower rank has not consumed yet, because its own next write into that
 // region needs the slower rank's contribution to an earlier site of the next step.
 //
+// The sum x_in + p_0 + ... + p_{N-1} runs in the same order on every rank from the same words,
+// so the residual stream stays bitwise identical across ranks.
+//
 // The vocabulary-parallel LM head pushes each rank's packed (logit, global index) maximum the
-// same way; every rank then reduces the N keys to the token id.
+// same way (two flagged words per key); every rank then reduces the N keys to the token id.
 //
 // Every wait is bounded (status word HK_ERR_PEER_TIMEOUT, then the kernel carries on with what
 // it has): a rank that stopped cannot hang the others' GPUs.
+#include <cooperative_groups.h>
+
 #include "decode_ops.cuh"
 #include "tp.cuh"
 
+namespace cg = cooperative_groups;
+
 namespace hk {
-
-__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-
-// Bounded wait by one thread for counter >= target.
-__device__ __forceinline__ bool wait_arrivals(const unsigned long long* counter, unsigned long long target, int* status) {
-  for (uint32_t i = 0; i < (1u << 24); ++i) {
-    if (ld_acquire_sys_u64(counter) >= target) return true;
-    if (i > 64) __nanosleep(64);
-  }
-  set_error(status, HK_ERR_PEER_TIMEOUT);
-  return false;
-}
 
 __global__ void tp_begin_kernel(int* epoch) {
   pdl_wait();
@@ -49,70 +40,109 @@ __global__ void tp_begin_kernel(int* epoch) {
 
 void tp_begin_launch(int* epoch, cudaStream_t s, bool pdl) { launch(tp_begin_kernel, dim3(1), dim3(32), 0, s, pdl, epoch); }
 
+constexpr int kTpCluster = 8;   // CTAs per row (one cluster)
+constexpr int kTpMaxE = 4;      // elements per thread: K <= kTpCluster * 256 * kTpMaxE
+constexpr int kTpMaxRanks = 8;
+
 // Consumer: x_out = x_in + sum over ranks of the partials, then RMSNorm (weight w) -> q8 blocks.
-// Grid (ceil(K / 256), rows); every CTA sums the whole row (for the norm) and writes its slice.
-__global__ void __launch_bounds__(256) tp_allreduce_rmsnorm_q8_kernel(TpReduceArgs a) {
-  __shared__ float red[32];
-  __shared__ int ok_s;
+// Grid (kTpCluster, rows), clusters of kTpCluster CTAs along x; CTA c owns elements
+// [c * K / C, (c + 1) * K / C) of its row, 256 threads striding over them (a warp owns whole
+// 32-element q8 blocks).
+__global__ void __cluster_dims__(kTpCluster, 1, 1) __launch_bounds__(256)
+    tp_allreduce_rmsnorm_q8_kernel(TpReduceArgs a) {
+  __shared__ float red[8];
+  __shared__ float part_ss;
   pdl_wait();
-  const int r = blockIdx.y, tid = threadIdx.x, lane = tid & 31;
-  if (tid == 0) {
-    const unsigned long long target = (unsigned long long)(*a.epoch) * (unsigned long long)a.producer_ctas * a.n;
-    ok_s = wait_arrivals(a.counter, target, a.status);
-  }
-  __syncthreads();
-  const int K = a.K;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int c = (int)cluster.block_rank();
+  const int r = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int K = a.K, chunk = K / kTpCluster, base = c * chunk, n = a.n;
+  const uint32_t flag = (uint32_t)*a.epoch;
+  const unsigned long long deadline = global_ns() + kTpWaitNs;
+  const unsigned long long* rr = a.recv + (int64_t)r * K;
   const float* xr = a.x_in + (int64_t)r * a.x_stride;
-  float ss = 0.f, mine = 0.f;
-  const int i_mine = blockIdx.x * 256 + tid;
-  for (int e = tid * 4; e < K; e += 1024) {
-    float4 v = *reinterpret_cast<const float4*>(xr + e);
-    for (int p = 0; p < a.n; ++p) {
-      const float4 q = __ldcg(reinterpret_cast<const float4*>(a.recv + (int64_t)p * a.rank_stride + (int64_t)r * K + e));
-      v.x += q.x;
-      v.y += q.y;
-      v.z += q.z;
-      v.w += q.w;
+
+  // issue every load first (independent loads in flight), then settle the stragglers
+  uint2 w[kTpMaxE][kTpMaxRanks];
+  float v[kTpMaxE];
+#pragma unroll
+  for (int j = 0; j < kTpMaxE; ++j) {
+    const bool on = j * 256 + warp * 32 < chunk;
+    const int e = base + j * 256 + tid;
+    v[j] = on ? xr[e] : 0.f;
+#pragma unroll
+    for (int p = 0; p < kTpMaxRanks; ++p)
+      if (on && p < n) w[j][p] = ll_load(rr + (int64_t)p * a.rank_stride + e);
+  }
+  bool ok = true;
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < kTpMaxE; ++j) {
+    const bool on = j * 256 + warp * 32 < chunk;
+    const int e = base + j * 256 + tid;
+#pragma unroll
+    for (int p = 0; p < kTpMaxRanks; ++p) {
+      if (on && p < n) {
+        ll_settle(w[j][p], rr + (int64_t)p * a.rank_stride + e, flag, deadline, ok);
+        v[j] += __uint_as_float(w[j][p].x);
+      }
     }
-    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    ss += v[j] * v[j];
   }
-  // this thread's own element of the CTA's slice (same sum, same order)
-  if (i_mine < K) {
-    float v = xr[i_mine];
-    for (int p = 0; p < a.n; ++p) v += __ldcg(a.recv + (int64_t)p * a.rank_stride + (int64_t)r * K + i_mine);
-    mine = v;
+  if (!ok) set_error(a.status, HK_ERR_PEER_TIMEOUT);
+  ss = warp_sum(ss);
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  if (tid == 0) {
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) t += red[i];
+    part_ss = t;
   }
-  ss = block_sum(ss, red);
-  const float scale = rsqrtf(ss / K + a.eps);
+  cluster.sync();
+  float total = 0.f;
+#pragma unroll
+  for (int i = 0; i < kTpCluster; ++i) total += *cluster.map_shared_rank(&part_ss, i);
+  cluster.sync();  // no CTA leaves while another still reads its partial
+  const float scale = rsqrtf(total / K + a.eps);
   pdl_launch();
-  if (i_mine < K) {
-    a.x_out[(int64_t)r * a.x_stride + i_mine] = mine;
-    float v = mine * scale;
-    if (a.w) v *= a.w[i_mine];
-    const float amax = warp_max(fabsf(v));
+#pragma unroll
+  for (int j = 0; j < kTpMaxE; ++j) {
+    if (j * 256 + warp * 32 >= chunk) continue;  // warp-uniform
+    const int e = base + j * 256 + tid;
+    a.x_out[(int64_t)r * a.x_stride + e] = v[j];
+    float y = v[j] * scale;
+    if (a.w) y *= a.w[e];
+    const float amax = warp_max(fabsf(y));
     const float d = amax / 127.f;
-    const int q = amax > 0.f ? __float2int_rn(v / d) : 0;
+    const int q = amax > 0.f ? __float2int_rn(y / d) : 0;
     const float qsum = warp_sum((float)q);
-    a.xq[(int64_t)r * K + i_mine] = (int8_t)q;
+    a.xq[(int64_t)r * K + e] = (int8_t)q;
     if (lane == 0) {
-      a.xd[(int64_t)r * (K / 32) + (i_mine >> 5)] = d;
-      a.xs[(int64_t)r * (K / 32) + (i_mine >> 5)] = d * qsum;
+      a.xd[(int64_t)r * (K / 32) + (e >> 5)] = d;
+      a.xs[(int64_t)r * (K / 32) + (e >> 5)] = d * qsum;
     }
   }
-  (void)ok_s;
 }
 
 void tp_allreduce_rmsnorm_q8_launch(const TpReduceArgs& a, int rows, cudaStream_t s, bool pdl) {
-  if (a.K % 256 || a.x_stride % 4) throw std::runtime_error("tp all-reduce norm: K must be a multiple of 256");
-  launch(tp_allreduce_rmsnorm_q8_kernel, dim3(a.K / 256, rows), dim3(256), 0, s, pdl, a);
+  if (a.K % (32 * kTpCluster) || a.K > kTpCluster * 256 * kTpMaxE || a.x_stride % 4)
+    throw std::runtime_error("tp all-reduce norm: K must be a multiple of 256 and at most 8192");
+  if (a.n < 1 || a.n > kTpMaxRanks) throw std::runtime_error("tp all-reduce norm: 1..8 ranks");
+  // the cluster shape is static (__cluster_dims__), so this is a plain launch
+  launch(tp_allreduce_rmsnorm_q8_kernel, dim3(kTpCluster, rows), dim3(256), 0, s, pdl, a);
 }
 
 // Vocabulary-parallel greedy: local best packed key per row (from the fused LM-head slots,
 // already holding global indices) -> pushed to every rank -> max of the N keys -> token id.
 __global__ void __launch_bounds__(256) tp_argmax_kernel(TpArgmaxArgs a) {
   __shared__ unsigned long long best_s[8];
+  __shared__ uint32_t flag_s;
   pdl_wait();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) flag_s = (uint32_t)(++a.uses[0]);  // this site's own round count (greedy steps only)
+  __syncthreads();
+  const uint32_t flag = flag_s;
   for (int r = 0; r < a.rows; ++r) {
     unsigned long long* sl = a.slots + (int64_t)r * kArgmaxSlots;
     unsigned long long best = 0;
@@ -130,29 +160,29 @@ __global__ void __launch_bounds__(256) tp_argmax_kernel(TpArgmaxArgs a) {
     __syncthreads();
     if (tid < a.n) {
       unsigned long long b = 0;
-      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) b = best_s[w] > b ? best_s[w] : b;
-      // push this rank's key for row r into rank tid's key region, slot [me][r]
-      a.keys[tid][(int64_t)a.me * a.max_rows + r] = b;
+      for (int wi = 0; wi < (int)(blockDim.x >> 5); ++wi) b = best_s[wi] > b ? best_s[wi] : b;
+      // this rank's key for row r -> rank tid's key region, words [me][r][0..1]
+      unsigned long long* dst = a.keys[tid] + ((int64_t)a.me * a.max_rows + r) * 2;
+      ll_store(dst, (uint32_t)(b >> 32), flag);
+      ll_store(dst + 1, (uint32_t)(b & 0xFFFFFFFFull), flag);
     }
     __syncthreads();
   }
-  TpSite site{a.counters, a.me, a.n};
-  tp_signal(site);
-  if (tid == 0) {
-    // this site has its own use count (greedy steps only), kept by this single-CTA kernel
-    const int uses = ++a.uses[0];
-    const unsigned long long target = (unsigned long long)uses * (unsigned long long)a.n;
-    wait_arrivals(a.counter_local, target, a.status);
-  }
-  __syncthreads();
+  const unsigned long long deadline = global_ns() + kTpWaitNs;
+  bool ok = true;
   for (int r = tid; r < a.rows; r += blockDim.x) {
     unsigned long long b = 0;
     for (int p = 0; p < a.n; ++p) {
-      const unsigned long long k = __ldcg(a.keys_local + (int64_t)p * a.max_rows + r);
+      const unsigned long long* src = a.keys_local + ((int64_t)p * a.max_rows + r) * 2;
+      uint2 hi = ll_load(src), lo = ll_load(src + 1);
+      ll_settle(hi, src, flag, deadline, ok);
+      ll_settle(lo, src + 1, flag, deadline, ok);
+      const unsigned long long k = ((unsigned long long)hi.x << 32) | lo.x;
       b = k > b ? k : b;
     }
     a.out[r] = b == 0ull ? 0 : (int)(0xFFFFFFFFu - (uint32_t)(b & 0xFFFFFFFFull));
   }
+  if (!ok) set_error(a.status, HK_ERR_PEER_TIMEOUT);
   pdl_launch();
 }
 

@@ -77,7 +77,10 @@ class Engine:
         # one block-table row beyond max_batch: scratch sequences (embeddings) never starve
         kv = PagedKVCache(cfg.layers, cfg.n_kv_heads, cfg.head_dim, num_blocks, block_size, max_batch + 1,
                           -(-max_ctx // block_size), device)
-        model = LlamaModel(cfg, weights, kv, max_rows=max(max_rows, max_batch), device=device, tp=tp)
+        # one forward holds a whole prefill budget (the tensor-core GEMMs and prefill attention
+        # want long row runs)
+        model = LlamaModel(cfg, weights, kv, max_rows=max(max_rows, max_batch, max_prefill_tokens), device=device,
+                           tp=tp)
         return Engine(cfg, model, kv, max_batch=max_batch, max_prefill_tokens=max_prefill_tokens, policy=policy)
 
     @staticmethod
@@ -137,6 +140,8 @@ class Engine:
                 sample_rows.append((it, len(ids) - 1))
         n = len(ids)
         decode_only = all(it.p1 - it.p0 == 1 for it in items)
+        if hasattr(m, "long_runs"):
+            m.long_runs = max((it.p1 - it.p0 for it in items), default=0) >= 16
         greedy = all(it.greedy for it, _ in sample_rows)
         mode = "greedy" if greedy else "none"
         sampled: List[int] = []

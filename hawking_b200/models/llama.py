@@ -214,7 +214,11 @@ class LlamaModel:
         self.part_o = torch.zeros(cap * nh * hd, device=self.dev)
         self.part_lse = torch.zeros(cap * nh, device=self.dev)
         self.attn_counters = torch.zeros(R * nkv, dtype=torch.int32, device=self.dev)
-        self.logits = torch.zeros(R, weights.lm_head.N, device=self.dev)
+        self.max_logit_rows = min(R, 256)  # rows whose logits one forward can return
+        self.logits = torch.zeros(self.max_logit_rows, weights.lm_head.N, device=self.dev)
+        # set by the caller when the forward's rows hold long runs of one sequence (prefill chunks):
+        # attention then runs on the tensor-core prefill kernel instead of the split-KV decode kernel
+        self.long_runs = False
         if tp is not None:
             self.x2 = torch.zeros(R, H, device=self.dev)       # second residual buffer (push all-reduce)
             self.partial = torch.zeros(R, H, device=self.dev)  # prefill partial sums (NCCL all-reduce)
@@ -301,6 +305,8 @@ class LlamaModel:
                 ops.advance(inp.ids, self.next_ids, inp.positions, inp.row_ctx, rows)
             return
         nl = n_logits or rows
+        if nl > self.max_logit_rows:
+            raise ValueError(f"forward: logits for {nl} rows requested, at most {self.max_logit_rows}")
         if tp is not None:
             self._lm_head_tp(rows, nl, n_logits, tc, sample)
             if advance:
@@ -342,6 +348,10 @@ class LlamaModel:
                         cfg.rope_style, self.q[:rows], kv.k[l], kv.v[l], cfg.n_heads, cfg.n_kv_heads,
                         cfg.head_dim, kv.block_size, bias=lw.qkv_bias, q_norm=lw.q_norm, k_norm=lw.k_norm,
                         eps=cfg.eps, block_tables=kv.block_tables, row_seq=inp.row_seq[:rows])
+        if self.long_runs and rows > GEMV_COLS and cfg.head_dim in (64, 128):
+            ops.attention_prefill(self.q[:rows], kv.k[l], kv.v[l], kv.block_tables, inp.row_seq[:rows],
+                                  inp.row_ctx[:rows], self.scale, out_q8=out_q8, out_bf16=out_bf16)
+            return
         ops.attention_decode(self.q[:rows], kv.k[l], kv.v[l], kv.block_tables, inp.row_seq[:rows],
                              inp.row_ctx[:rows], self.scale, splits, self.part_o, self.part_lse,
                              out_q8=out_q8, out_bf16=out_bf16, counters=self.attn_counters)
@@ -377,19 +387,18 @@ class LlamaModel:
             off += wt.N
         self._rope_attention(l, lw, rows, splits, out_q8=self.att.view(rows))
         ops.gemv_push(lw.wo, self._q8_slice(self.att, 0, rows), tp, 2 * l)
-        ops.tp_allreduce_rmsnorm_q8(tp, 2 * l, xa_res, xb_res, lw.ffn_norm, cfg.eps, self.xa.view(rows),
-                                    producer_ctas=-(-lw.wo.N // 8))
+        ops.tp_allreduce_rmsnorm_q8(tp, 2 * l, xa_res, xb_res, lw.ffn_norm, cfg.eps, self.xa.view(rows))
         ops.gemv_swiglu(lw.w_gate, lw.w_up, self.xa_view(0, rows), self._q8_slice(self.hq, 0, rows))
         ops.gemv_push(lw.w_down, self._q8_slice(self.hq, 0, rows, lw.w_down.K), tp, 2 * l + 1)
         nxt = w.layers[l + 1].attn_norm if l + 1 < len(w.layers) else w.out_norm
-        ops.tp_allreduce_rmsnorm_q8(tp, 2 * l + 1, xb_res, xa_res, nxt, cfg.eps, self.xa.view(rows),
-                                    producer_ctas=-(-lw.w_down.N // 8))
+        ops.tp_allreduce_rmsnorm_q8(tp, 2 * l + 1, xb_res, xa_res, nxt, cfg.eps, self.xa.view(rows))
 
     def _allreduce_partial_tc(self, rows):
         """Prefill (tensor-core path): NCCL all-reduce of this rank's partial, added to x."""
         import torch.distributed as dist
         p = self.partial[:rows]
-        dist.all_reduce(p, group=self.tp.group)
+        if self.tp.world > 1:
+            dist.all_reduce(p, group=self.tp.group)
         self.x[:rows].add_(p)
 
     def _lm_head_tp(self, rows, nl, n_logits, tc, sample):
@@ -454,12 +463,17 @@ class LlamaModel:
         kv.sync_tables([seq_id])
         r = kv.row(seq_id)
         out = torch.empty(n, self.logits.shape[1], device=self.dev)  # this rank's vocabulary slice under TP
-        for c0 in range(0, n, self.max_rows):
-            c1 = min(n, c0 + self.max_rows)
-            pos = list(range(start_pos + c0, start_pos + c1))
-            self.inp.upload(tokens[c0:c1], pos, [0] * (c1 - c0), [r] * (c1 - c0), [p + 1 for p in pos])
-            self.forward(c1 - c0, "none", n_logits=0)
-            out[c0:c1] = self.logits[: c1 - c0]
+        step = self.max_logit_rows
+        self.long_runs = True
+        try:
+            for c0 in range(0, n, step):
+                c1 = min(n, c0 + step)
+                pos = list(range(start_pos + c0, start_pos + c1))
+                self.inp.upload(tokens[c0:c1], pos, [0] * (c1 - c0), [r] * (c1 - c0), [p + 1 for p in pos])
+                self.forward(c1 - c0, "none", n_logits=0)
+                out[c0:c1] = self.logits[: c1 - c0]
+        finally:
+            self.long_runs = False
         return out
 
     def xa_view(self, c0, c1, K=None):

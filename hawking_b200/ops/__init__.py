@@ -79,7 +79,7 @@ def gemv_push(w: QWeight, x: Q8Act, tp, site: int, bias=None):
     (tensor-parallel all-reduce push, see parallel/tp.py)."""
     launches.add()
     kernels().gemv(w.fmt, EPI_PUSH, w.planes, [], w.N, w.K, x.q, x.d, x.s, None, bias, None, None, None, None, None,
-                   -1.0, PDL, None, 0, tp.push_recv[site], tp.push_counters[site])
+                   -1.0, PDL, None, 0, tp.push_recv[site], tp.epoch)
 
 
 def tp_begin(tp):
@@ -87,23 +87,20 @@ def tp_begin(tp):
     kernels().tp_begin(tp.epoch, PDL)
 
 
-def tp_allreduce_rmsnorm_q8(tp, site: int, x_in: torch.Tensor, x_out: torch.Tensor, w, eps: float, out: Q8Act,
-                            producer_ctas: int):
+def tp_allreduce_rmsnorm_q8(tp, site: int, x_in: torch.Tensor, x_out: torch.Tensor, w, eps: float, out: Q8Act):
     """x_out = x_in + sum of every rank's partials at ``site``; then RMSNorm -> q8 (``out``)."""
     launches.add()
-    kernels().tp_allreduce_rmsnorm_q8(x_in, x_out, tp.recv_local(site), tp.rank_stride, tp.world,
-                                       tp.counter_local(site), tp.epoch, producer_ctas, w, eps, out.q, out.d, out.s,
-                                       tp.status, PDL)
+    kernels().tp_allreduce_rmsnorm_q8(x_in, x_out, tp.recv_local(site), tp.rank_stride, tp.world, tp.epoch, w, eps,
+                                       out.q, out.d, out.s, tp.status, PDL)
 
 
 def tp_argmax(tp, slots: torch.Tensor, rows: int, out: torch.Tensor):
     """Global greedy ids from every rank's fused LM-head keys (vocabulary-parallel)."""
     launches.add()
-    site = tp.argmax_site
     if rows > tp.key_rows:
         raise ValueError(f"tp_argmax: {rows} rows exceed the key region ({tp.key_rows})")
-    kernels().tp_argmax(slots, rows, tp.key_rows, tp.keys_table, tp.base + tp.keys_off, tp.push_counters[site],
-                        tp.counter_local(site), tp.argmax_uses, tp.rank, out, tp.status, PDL)
+    kernels().tp_argmax(slots, rows, tp.key_rows, tp.keys_table, tp.base + tp.keys_off, tp.argmax_uses, tp.rank, out,
+                        tp.status, PDL)
 
 
 def argmax_finalize(slots: torch.Tensor, rows: int, out: torch.Tensor):
@@ -173,6 +170,16 @@ def attention_decode(q, k_cache, v_cache, block_tables, row_seq, row_ctx, scale,
     kernels().attention_decode(q, k_cache, v_cache, block_tables, row_seq, row_ctx, scale, num_splits, part_o,
                                part_lse, out, out_q8.q if out_q8 else None, out_q8.d if out_q8 else None,
                                out_q8.s if out_q8 else None, sinks, out_bf16, counters, PDL, cluster)
+
+
+def attention_prefill(q, k_cache, v_cache, block_tables, row_seq, row_ctx, scale, out=None,
+                      out_q8: Optional[Q8Act] = None, sinks=None, out_bf16=None):
+    """Causal paged attention for many rows on the tensor cores (flash-style, 64-row tiles per
+    query head); rows of different sequences may share a launch."""
+    launches.add(1)
+    kernels().attention_prefill(q, k_cache, v_cache, block_tables, row_seq, row_ctx, scale, out,
+                                out_q8.q if out_q8 else None, out_q8.d if out_q8 else None,
+                                out_q8.s if out_q8 else None, sinks, out_bf16, PDL)
 
 
 def argmax(logits: torch.Tensor, out: torch.Tensor):

@@ -9,8 +9,8 @@ region over NVLink and the next RMSNorm sums them; greedy sampling reduces per-r
 keys the same way. Prefill (tensor-core path) all-reduces its partials with NCCL.
 
 ``TPComm`` owns the shared buffers: one CUDA-IPC region per rank (receive regions of every
-all-reduce site, the argmax key region, arrival counters), mapped into every other rank's process.
-No NVLink multicast object is created.
+all-reduce site and the argmax key region, all as flagged 8-byte words), mapped into every other
+rank's process. No NVLink multicast object is created.
 
 Parity: the reference has no tensor parallelism (one Apple GPU); the sharding plan follows the
 north-star requirement of column-parallel QKV/gate/up and row-parallel O/down with a vocabulary-
@@ -126,19 +126,20 @@ class TPComm:
         self.max_rows, self.width, self.key_rows = max_rows, width, key_rows
         self.dev = torch.device(device)
         self.group = group
-        self.rank_stride = max_rows * width                       # floats per source rank
-        self.site_floats = world * self.rank_stride
-        recv_bytes = n_sites * self.site_floats * 4
+        # flagged 8-byte words: value | flag << 32 (see the kernels)
+        self.rank_stride = max_rows * width                       # words per source rank
+        self.site_words = world * self.rank_stride
+        recv_bytes = n_sites * self.site_words * 8
         self.keys_off = recv_bytes
-        keys_bytes = world * key_rows * 8
-        self.cnt_off = self.keys_off + keys_bytes
-        total = self.cnt_off + (n_sites + 1) * 8
-        total = (total + 255) // 256 * 256
+        keys_bytes = world * key_rows * 2 * 8                     # two flagged words per key
+        total = (self.keys_off + keys_bytes + 255) // 256 * 256
         with torch.cuda.device(self.dev):
             self.base = K.ipc_malloc(total)
             handle = bytes(K.ipc_handle(self.base))
-        handles: List[bytes] = [None] * world
-        dist.all_gather_object(handles, handle, group=group)
+        handles: List[bytes] = [handle]
+        if world > 1:
+            handles = [None] * world
+            dist.all_gather_object(handles, handle, group=group)
         self.ptrs = []
         with torch.cuda.device(self.dev):
             for p, h in enumerate(handles):
@@ -150,20 +151,15 @@ class TPComm:
         def table(vals):
             return torch.tensor(vals, dtype=torch.int64, device=self.dev)
 
-        # per site: where MY partial goes in every rank's region, and every rank's counter
-        self.push_recv = [table([self.ptrs[p] + 4 * (s * self.site_floats + rank * self.rank_stride)
+        # per site: where MY partial goes in every rank's region
+        self.push_recv = [table([self.ptrs[p] + 8 * (s * self.site_words + rank * self.rank_stride)
                                  for p in range(world)]) for s in range(n_sites)]
-        self.push_counters = [table([self.ptrs[p] + self.cnt_off + 8 * s for p in range(world)])
-                              for s in range(n_sites + 1)]
         self.keys_table = table([self.ptrs[p] + self.keys_off for p in range(world)])
         self.closed = False
 
     # local addresses
     def recv_local(self, site: int) -> int:
-        return self.base + 4 * site * self.site_floats
-
-    def counter_local(self, site: int) -> int:
-        return self.base + self.cnt_off + 8 * site
+        return self.base + 8 * site * self.site_words
 
     @property
     def argmax_site(self) -> int:
@@ -178,13 +174,15 @@ class TPComm:
         if self.closed:
             return
         torch.cuda.synchronize(self.dev)
-        dist.barrier(group=self.group)
+        if self.world > 1:
+            dist.barrier(group=self.group)
         K = kernels()
         with torch.cuda.device(self.dev):
             for p, ptr in enumerate(self.ptrs):
                 if p != self.rank:
                     K.ipc_close(ptr)
-        dist.barrier(group=self.group)
+        if self.world > 1:
+            dist.barrier(group=self.group)
         with torch.cuda.device(self.dev):
             K.ipc_free(self.base)
         self.closed = True

@@ -109,7 +109,8 @@ def test_rope_append(style, hd):
     kr = rope_ref(qkv[:, nh * hd:(nh + nkv) * hd].view(R, nkv, hd), pos.long(), 10000.0, hd, style)
     torch.testing.assert_close(q, qr, rtol=1e-5, atol=1e-5)
     for r, s in enumerate(slots.tolist()):
-        torch.testing.assert_close(kc[s // bs, :, s % bs].float(), kr[r].bfloat16().float())
+        # bf16 of the kernel's fp32 rotation: within one bf16 rounding of the fp32 reference
+        torch.testing.assert_close(kc[s // bs, :, s % bs].float(), kr[r], rtol=2 ** -8, atol=1e-5)
         torch.testing.assert_close(vc[s // bs, :, s % bs].float(),
                                    qkv[r, (nh + nkv) * hd:].view(nkv, hd).bfloat16().float())
 
@@ -156,6 +157,33 @@ def test_attention_decode(nh, nkv, hd, splits):
     ref = _paged_attention_ref(q, kc, vc, tables, row_seq, row_ctx, scale).reshape(R, -1)
     torch.testing.assert_close(out, ref, rtol=2e-3, atol=2e-3)
     assert ((oq.dequantize() - ref).abs() <= oq.d.repeat_interleave(32, 1) * 0.51 + 3e-3).all()
+
+
+@pytest.mark.parametrize("nh,nkv,hd,bs", [(8, 2, 64, 16), (32, 8, 128, 64), (8, 8, 128, 16)])
+def test_attention_prefill(nh, nkv, hd, bs):
+    """Tensor-core prefill attention vs the fp32 reference: two sequences' runs (one starting
+    mid-tile at position 37), a lone decode-style row, and a run split across 64-row tiles."""
+    g = torch.Generator(device=DEV).manual_seed(nh * hd + bs)
+    nblk = 48 * 64 // bs
+    kc = torch.randn(nblk, nkv, bs, hd, device=DEV, generator=g).bfloat16()
+    vc = torch.randn(nblk, nkv, bs, hd, device=DEV, generator=g).bfloat16()
+    perm = torch.randperm(nblk, device=DEV, generator=g).int()
+    tables = torch.stack([perm[: nblk // 2], perm[nblk // 2:]]).contiguous()
+    seq = [0] * 100 + [1] * 134 + [0]
+    ctx = [p + 1 for p in range(100)] + [p + 1 for p in range(37, 171)] + [100]
+    R = len(seq)
+    row_seq = torch.tensor(seq, dtype=torch.int32, device=DEV)
+    row_ctx = torch.tensor(ctx, dtype=torch.int32, device=DEV)
+    q = torch.randn(R, nh, hd, device=DEV, generator=g)
+    scale = 1 / math.sqrt(hd)
+    out = torch.zeros(R, nh * hd, device=DEV)
+    outb = torch.zeros(R, nh * hd, dtype=torch.bfloat16, device=DEV)
+    oq = Q8Act(R, nh * hd, DEV)
+    ops.attention_prefill(q, kc, vc, tables, row_seq, row_ctx, scale, out=out, out_q8=oq, out_bf16=outb)
+    ref = _paged_attention_ref(q, kc, vc, tables, row_seq, row_ctx, scale).reshape(R, -1)
+    torch.testing.assert_close(out, ref, rtol=3e-2, atol=3e-2)  # q and P are rounded to bf16
+    torch.testing.assert_close(outb.float(), ref, rtol=4e-2, atol=4e-2)
+    assert ((oq.dequantize() - out).abs() <= oq.d.repeat_interleave(32, 1) * 0.51 + 1e-4).all()
 
 
 @pytest.mark.parametrize("nb", [1, 3])
