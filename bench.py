@@ -121,6 +121,9 @@ def bench_qwen_next(args):
             kv.drop(10 + i)
         return e0.elapsed_time(e1) / K, cs.result
 
+    if args.profile_step:
+        profile_one_step(m, kv, ctx)
+        return 0
     ms1, clocks = timed(1)
     launches = m.launches_per_graph
     ms8, clocks8 = timed(8)
@@ -146,6 +149,23 @@ def bench_qwen_next(args):
     }
     print(json.dumps(out))
     return 0
+
+
+def profile_one_step(m, kv, ctx):
+    """One eager bs1 decode step between cudaProfilerStart/Stop (after warm-up), for
+    ``ncu --profile-from-start off``."""
+    import torch
+    kv.bm.reserve(10, ctx + 16)
+    kv.sync_tables([10])
+    m.inp.upload([1], [ctx], [0], [kv.row(10)], [ctx + 1])
+    for _ in range(3):
+        m.forward(1, "greedy")
+    torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStart()
+    m.forward(1, "greedy")
+    torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStop()
+    print(json.dumps({"profile_step": True}))
 
 
 def bench_deepseek(args):
@@ -197,6 +217,9 @@ def bench_deepseek(args):
             kv.drop(10 + i)
         return e0.elapsed_time(e1) / K, cs.result
 
+    if args.profile_step:
+        profile_one_step(m, kv, ctx)
+        return 0
     ms1, clocks = timed(1)
     launches = m.launches_per_graph
     ms8, clocks8 = timed(8)
@@ -303,10 +326,11 @@ def main():
         for _ in range(W):
             m.graph_forward(nseq, "greedy", advance=True)
         torch.cuda.synchronize()
-        barrier()
-        torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with ClockSampler(local, period_ms=50) as cs:
+            # the barrier comes after every rank's sampler is up, so all ranks start together
+            barrier()
+            torch.cuda.synchronize()
             e0.record()
             for _ in range(K):
                 m.graph_forward(nseq, "greedy", advance=True)

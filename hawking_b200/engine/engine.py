@@ -54,6 +54,7 @@ class Engine:
                  policy: int = 0, use_graphs: bool = True):
         self.cfg, self.model, self.kv = cfg, model, kv
         self.max_batch = max_batch
+        self.max_prefill_tokens = max_prefill_tokens
         self.sched = native().Scheduler(kv.bm, max_batch, max_prefill_tokens, policy)
         self.requests: Dict[int, RequestState] = {}
         self._ids = itertools.count(1)
@@ -145,7 +146,7 @@ class Engine:
         greedy = all(it.greedy for it, _ in sample_rows)
         mode = "greedy" if greedy else "none"
         sampled: List[int] = []
-        R = m.max_rows
+        R = getattr(m, "row_limit", m.max_rows)
         for c0 in range(0, n, R):
             c1 = min(n, c0 + R)
             self.stats.h2d_bytes += m.inp.upload(ids[c0:c1], pos[c0:c1], slots[c0:c1], rseq[c0:c1], rctx[c0:c1])

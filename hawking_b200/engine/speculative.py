@@ -52,7 +52,7 @@ class SpeculativeDecoder:
 
     def _forward_rows(self, sid: int, tokens: Sequence[int], p0: int, logits_row: Optional[int]) -> List[int]:
         """Run ``tokens`` at positions p0.. of sequence ``sid``; returns the greedy id of every row
-        (logits_row=None) or of the single row ``logits_row``."""
+        (logits_row=None), of the single row ``logits_row``, or nothing (logits_row=-1)."""
         eng, m, kv = self.engine, self.engine.model, self.engine.kv
         n = len(tokens)
         if not kv.bm.reserve(sid, p0 + n):
@@ -62,6 +62,12 @@ class SpeculativeDecoder:
         slots = kv.bm.slots(sid, p0, p0 + n)
         pos = list(range(p0, p0 + n))
         eng.stats.h2d_bytes += m.inp.upload(list(tokens), pos, slots, [r] * n, [p + 1 for p in pos])
+        m.long_runs = n >= 16  # the engine's rule: same kernels, same logits as plain decode
+        if logits_row == -1:
+            m.forward(n, "none", n_logits=-1)
+            m.long_runs = False
+            self.stats.forward_rows += n
+            return []
         if logits_row is None:
             m.forward(n, "greedy")
             k = n
@@ -69,6 +75,7 @@ class SpeculativeDecoder:
             m.logit_rows[:1].copy_(torch.tensor([logits_row], dtype=torch.int32), non_blocking=True)
             m.forward(n, "greedy", n_logits=1)
             k = 1
+        m.long_runs = False
         ids = m.next_ids[:k].cpu().tolist()
         eng.stats.d2h_bytes += 4 * k
         self.stats.forward_rows += n
@@ -83,12 +90,12 @@ class SpeculativeDecoder:
         m.force_splits = m.num_splits(1)
         try:
             prompt = [int(t) for t in prompt]
-            R = m.max_rows
+            R = min(getattr(m, "row_limit", m.max_rows), eng.max_prefill_tokens)
             tok = None
             for c0 in range(0, len(prompt), R):  # prefill in the same chunks as the engine
                 c1 = min(len(prompt), c0 + R)
                 last = c1 == len(prompt)
-                ids = self._forward_rows(sid, prompt[c0:c1], c0, (c1 - c0 - 1) if last else None)
+                ids = self._forward_rows(sid, prompt[c0:c1], c0, (c1 - c0 - 1) if last else -1)
                 tok = ids[0] if last else None
             history = prompt + [tok]
             out = [tok]

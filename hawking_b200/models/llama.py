@@ -259,6 +259,14 @@ class LlamaModel:
         for c0 in range(0, rows, GEMV_COLS):
             fn(c0, min(rows, c0 + GEMV_COLS))
 
+    @property
+    def row_limit(self) -> int:
+        """Most rows one forward takes: all of ``max_rows``, except under tensor parallelism
+        without the tensor-core path, whose push all-reduce sites hold GEMV_COLS rows."""
+        if self.tp is not None and not self.use_tensor_cores(GEMV_COLS + 1):
+            return GEMV_COLS
+        return self.max_rows
+
     def use_tensor_cores(self, rows: int) -> bool:
         l0 = self.w.layers[0]
         return rows > GEMV_COLS and all(w.fmt == GgmlType.Q4_K for w in l0.wqkv + [l0.wo]) and \
@@ -463,7 +471,7 @@ class LlamaModel:
         kv.sync_tables([seq_id])
         r = kv.row(seq_id)
         out = torch.empty(n, self.logits.shape[1], device=self.dev)  # this rank's vocabulary slice under TP
-        step = self.max_logit_rows
+        step = min(self.max_logit_rows, self.row_limit)
         self.long_runs = True
         try:
             for c0 in range(0, n, step):

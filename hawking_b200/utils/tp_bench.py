@@ -154,7 +154,8 @@ def step_mode(args, rank, world, dev):
     for l in range(cfg.layers):
         kv.k[l].normal_()
         kv.v[l].normal_()
-    kv.bm.reserve(7, ctx + 4096)
+    if not kv.bm.reserve(7, ctx + 64):
+        raise RuntimeError("KV pool too small")
     kv.sync_tables([7])
     res = {}
     for name, own, local in (("tp", False, False), ("own_slot", True, False), ("local_push", True, True)):
