@@ -34,7 +34,9 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=10)
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "torch"],
+                    help="ours | reference (the upstream project, unavailable here) | torch (in-box PyTorch "
+                         "cuBLAS + SDPA + NCCL baseline of the same Llama architecture, bf16 weights)")
     ap.add_argument("--model", default="llama3-8b")
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--ctx", type=int, default=2048)
@@ -245,12 +247,132 @@ def bench_deepseek(args):
     return 0
 
 
+def bench_torch(args):
+    """In-box library baseline (``--impl torch``): the same Llama-3-8B architecture and workload in
+    plain PyTorch (bf16 weights, cuBLAS, SDPA, NCCL tensor parallelism), CUDA-graph decode."""
+    import datetime
+    import statistics
+
+    import torch
+    import torch.distributed as dist
+    from hawking_b200.models.config import preset
+    from hawking_b200.utils.clocks import ClockSampler
+    from hawking_b200.utils.torch_baseline import TorchLlamaTP
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+    cfg = preset(args.model)
+    B, ctx, K, W = args.batch, args.ctx, args.steps, args.warmup
+    cap = ctx + W + 2 * K + 16  # warm-up, timed and end-to-end steps each advance every position
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_ranks(v):
+        if world > 1:
+            t = torch.tensor([v], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return t.item()
+        return v
+
+    def timed(nb):
+        m = TorchLlamaTP(cfg, rank, world, dev, nb, cap)
+        g = torch.Generator(device=dev).manual_seed(1)
+        for t in m.k + m.v:
+            t.normal_(0, 1, generator=g)
+        m.pos.fill_(ctx)
+        m.ids.random_(0, cfg.vocab, generator=g)
+        for _ in range(W):
+            m.decode_step()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local, period_ms=50) as cs:
+            barrier()
+            torch.cuda.synchronize()
+            e0.record()
+            for _ in range(K):
+                m.decode_step()
+            e1.record()
+            torch.cuda.synchronize()
+        ms = max_ranks(e0.elapsed_time(e1) / K)
+        # end to end: per step the ids go up from pinned memory and the next ids come back
+        host_in = torch.zeros(nb, dtype=torch.long).pin_memory()
+        host_out = torch.zeros(nb, dtype=torch.long).pin_memory()
+        barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(K):
+            m.ids.copy_(host_in, non_blocking=True)
+            m.decode_step()
+            host_out.copy_(m.next_ids, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+            host_in.copy_(host_out)
+        dt = max_ranks(time.perf_counter() - t0)
+        nbytes = m.nbytes
+        m.release()
+        del m
+        torch.cuda.empty_cache()
+        return ms, cs.result, nb * K / dt, nbytes
+
+    ms1, clocks, e2e1, wbytes = timed(B)
+    ms64, clocks64, _, _ = timed(64) if args.bs64 and B != 64 else (None, None, None, None)
+    # TTFT: eager prefill of a ctx-token prompt, next id read back to the host
+    m = TorchLlamaTP(cfg, rank, world, dev, 1, ctx + 8)
+    ttfts = []
+    for run in range(max(1, args.ttft_runs) + 1):
+        prompt = torch.randint(0, cfg.vocab, (1, ctx), generator=torch.Generator().manual_seed(100 + run))
+        torch.cuda.synchronize()
+        barrier()
+        t0 = time.perf_counter()
+        nxt = m.prefill(prompt.to(dev, non_blocking=True))
+        int(nxt[0].item())
+        dt = max_ranks(time.perf_counter() - t0)
+        if run:  # the first run warms up the kernels
+            ttfts.append(dt * 1000.0)
+    out = {
+        "impl": "torch",
+        "metric": METRIC,
+        "value": round(B * 1000.0 / ms1, 2), "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": round(ms1, 4), "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
+        "vs_baseline": None, "dtype": "bf16 weights and activations, fp32 softmax",
+        "data": "synthetic: random-init N(0,0.02) bf16 weights, random bf16 KV for a %d-token context, "
+                "uniform-random token ids" % ctx,
+        "config": {"model": "llama3-8b architecture, bf16 weights (no Q4_K kernel in PyTorch)",
+                   "global_batch": B, "seq_len": ctx, "parallelism": f"tp{world}",
+                   "l2": "inputs larger than L2: %.2f GB of weights per step per GPU" % (wbytes / 1e9),
+                   "attention": "decode: masked grouped-query batched GEMMs over a %d-slot cache; prefill: "
+                                "SDPA causal" % cap},
+        "clocks": clocks,
+        "e2e": {"value": round(e2e1, 2), "unit": "tok/s", "h2d_bytes_per_step": 8 * B, "d2h_bytes_per_step": 8 * B,
+                "api": "TorchLlamaTP.decode_step()"},
+        "gpu_launches": None,
+        "bs64": {"tok_s_aggregate": round(64 * 1000.0 / ms64, 1), "ms_per_step": round(ms64, 4),
+                 "clocks": clocks64} if ms64 else None,
+        "ttft_p50_ms": round(statistics.median(ttfts), 2),
+        "ttft_runs_ms": [round(t, 2) for t in ttfts],
+    }
+    if rank == 0:
+        print(json.dumps(out))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         if int(os.environ.get("RANK", "0")) == 0:
             reference_unavailable(args)
         return 0
+    if args.impl == "torch":
+        return bench_torch(args)
     if args.model == "qwen3-next":
         return bench_qwen_next(args)
     if args.model == "deepseek-v3":

@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <torch/extension.h>
 
+#include <climits>
+
 #include <stdexcept>
 #include <string>
 
@@ -104,8 +106,9 @@ void moe_mixed_gemv(int64_t epi, const Tensor& descs, int64_t base0, int64_t bas
                     const Tensor& counts, const Tensor& offsets, const Tensor& sorted, const Tensor& active,
                     const Tensor& n_active, int64_t max_active, const Tensor& xq, const Tensor& xd, const Tensor& xs,
                     const optional<Tensor>& oq, const optional<Tensor>& od, const optional<Tensor>& os,
-                    const optional<Tensor>& y, const optional<Tensor>& route_w, bool pdl) {
+                    const optional<Tensor>& y, const optional<Tensor>& route_w, bool pdl, int64_t routed_pairs) {
   hk::MoeMixedArgs a{};
+  a.routed_pairs = routed_pairs < 0 ? INT_MAX : (int)routed_pairs;
   a.desc = reinterpret_cast<const hk::MixedDesc*>(descs.data_ptr());
   a.desc_base0 = (int)base0;
   a.desc_base1 = (int)base1;
@@ -281,7 +284,8 @@ void register_model_kernels(py::module_& m) {
         py::arg("N"), py::arg("K"), py::arg("k"), py::arg("counts"), py::arg("offsets"), py::arg("sorted"),
         py::arg("active"), py::arg("n_active"), py::arg("max_active"), py::arg("xq"), py::arg("xd"), py::arg("xs"),
         py::arg("oq") = py::none(), py::arg("od") = py::none(), py::arg("os") = py::none(), py::arg("y") = py::none(),
-        py::arg("route_w") = py::none(), py::arg("pdl") = false);
+        py::arg("route_w") = py::none(), py::arg("pdl") = false,
+        py::arg("routed_pairs") = -1);
   m.def("deltanet_conv", &deltanet_conv, py::arg("qkvz"), py::arg("conv_w"), py::arg("conv_state"), py::arg("slot"),
         py::arg("kh"), py::arg("r"), py::arg("dk"), py::arg("dv"), py::arg("kc"), py::arg("eps"), py::arg("q"),
         py::arg("k"), py::arg("v"), py::arg("z"), py::arg("pdl") = false);

@@ -103,8 +103,9 @@ void moe_topk(const Tensor& logits, const c10::optional<Tensor>& bias, int64_t k
 
 void moe_align(const Tensor& ids, int64_t E, const Tensor& xq, const Tensor& xd, const Tensor& xs,
                const Tensor& counts, const Tensor& offsets, const Tensor& sorted, const Tensor& gq,
-               const Tensor& gd, const Tensor& gs, bool pdl) {
+               const Tensor& gd, const Tensor& gs, bool pdl, bool shared) {
   hk::MoeAlignArgs a{};
+  a.shared = shared ? 1 : 0;
   a.ids = ids.data_ptr<int>();
   a.T = (int)ids.size(0);
   a.k = (int)ids.size(1);
@@ -173,7 +174,8 @@ void register_more_kernels(py::module_& m) {
         py::arg("weights"), py::arg("pdl") = false);
   m.def("moe_align", &moe_align, py::arg("ids"), py::arg("E"), py::arg("xq"), py::arg("xd"), py::arg("xs"),
         py::arg("counts"), py::arg("offsets"), py::arg("sorted"), py::arg("gq"), py::arg("gd"), py::arg("gs"),
-        py::arg("pdl") = false);
+        py::arg("pdl") = false,
+        py::arg("shared") = false);
   m.def("moe_gemv", &moe_gemv, py::arg("fmt"), py::arg("epi"), py::arg("w0"), py::arg("w1"), py::arg("N"),
         py::arg("K"), py::arg("E"), py::arg("k"), py::arg("counts"), py::arg("offsets"), py::arg("sorted"),
         py::arg("xq"), py::arg("xd"), py::arg("xs"), py::arg("oq") = py::none(), py::arg("od") = py::none(),

@@ -240,12 +240,13 @@ struct MoeAlignArgs {
   const float* xd;
   const float* xs;
   int64_t x_stride_q, x_stride_s;
-  int* counts;           // [E]
-  int* offsets;          // [E]
-  int* sorted;           // [T*k] pair ids (t*k + j) grouped by expert
+  int* counts;           // [E] (+1 with `shared`)
+  int* offsets;          // [E] (+1 with `shared`)
+  int* sorted;           // [T*k] pair ids (t*k + j) grouped by expert (+T shared pairs)
   int8_t* gq;            // gathered activations [T*k, K] (sorted order)
   float* gd;
   float* gs;
+  int shared;            // 1: append expert E (the shared expert) with pairs T*k + t, one per token
 };
 void moe_align_launch(const MoeAlignArgs& a, cudaStream_t s, bool pdl);
 
@@ -314,6 +315,8 @@ struct MoeMixedArgs {
   float* y;                   // epi 1: residual rows of the tokens
   int64_t y_stride;
   const float* route_w;
+  int routed_pairs;           // pairs below this are routed (token pair / k, weight route_w[pair]);
+                              // the rest are shared-expert pairs (token pair - routed_pairs, weight 1)
 };
 void moe_mixed_gemv_launch(int epi, const MoeMixedArgs& a, int max_active, cudaStream_t s, bool pdl);
 void moe_active_launch(const int* counts, int E, int* active, int* n_active, cudaStream_t s, bool pdl);

@@ -219,7 +219,9 @@ __global__ void __launch_bounds__(256) moe_mixed_gemv_kernel(MoeMixedArgs a) {
       const float v = mixed_row_dot(tg, n, a.K, xq, xd, xs);
       if (lane == 0) {
         const int pair = a.sorted[sp];
-        atomicAdd(a.y + (int64_t)(pair / a.k) * a.y_stride + n, a.route_w[pair] * v);
+        const bool routed = pair < a.routed_pairs;
+        const int tok = routed ? pair / a.k : pair - a.routed_pairs;
+        atomicAdd(a.y + (int64_t)tok * a.y_stride + n, (routed ? a.route_w[pair] : 1.f) * v);
       }
     }
   }

@@ -172,24 +172,24 @@ void moe_topk_launch(const MoeTopkArgs& a, cudaStream_t s, bool pdl) {
 // One CTA. counts/offsets [E], sorted pairs [T*k] (pair = t*k + j), and the q8 activations of
 // each pair's token gathered in sorted order (gq [T*k, K], gd/gs [T*k, K/32]).
 __global__ void __launch_bounds__(1024) moe_align_kernel(MoeAlignArgs a) {
-  __shared__ int cnt[1024], off[1025];
+  __shared__ int cnt[1025], off[1026];
   pdl_wait();
   const int tid = threadIdx.x, P = a.T * a.k;
-  for (int e = tid; e < a.E; e += blockDim.x) cnt[e] = 0;
+  const int E1 = a.E + (a.shared ? 1 : 0), PS = P + (a.shared ? a.T : 0);
+  for (int e = tid; e < E1; e += blockDim.x) cnt[e] = 0;
   __syncthreads();
   for (int p = tid; p < P; p += blockDim.x) atomicAdd(&cnt[a.ids[p]], 1);
+  if (a.shared && tid == 0) cnt[a.E] = a.T;
   __syncthreads();
   if (tid == 0) {
     off[0] = 0;
-    for (int e = 0; e < a.E; ++e) off[e + 1] = off[e] + cnt[e];
+    for (int e = 0; e < E1; ++e) off[e + 1] = off[e] + cnt[e];
   }
   __syncthreads();
-  for (int e = tid; e < a.E; e += blockDim.x) {
+  for (int e = tid; e < E1; e += blockDim.x) {
     a.counts[e] = cnt[e];
     a.offsets[e] = off[e];
-    cnt[e] = 0;
   }
-  __syncthreads();
   // Stable placement: pairs of one expert keep token order (serial per expert bucket).
   if (tid < a.E) {
     const int e = tid;
@@ -197,17 +197,18 @@ __global__ void __launch_bounds__(1024) moe_align_kernel(MoeAlignArgs a) {
     for (int p = 0; p < P; ++p)
       if (a.ids[p] == e) a.sorted[pos++] = p;
   }
+  for (int t = tid; t < PS - P; t += blockDim.x) a.sorted[P + t] = P + t;  // shared bucket is last
   __syncthreads();
   // Gather q8 activations in sorted order.
   const int K = a.K;
-  for (int idx = tid; idx < P * (K / 16); idx += blockDim.x) {
+  for (int idx = tid; idx < PS * (K / 16); idx += blockDim.x) {
     const int sp = idx / (K / 16), c = idx % (K / 16);
-    const int tok = a.sorted[sp] / a.k;
+    const int pr = a.sorted[sp], tok = pr < P ? pr / a.k : pr - P;
     reinterpret_cast<int4*>(a.gq + (int64_t)sp * K)[c] = reinterpret_cast<const int4*>(a.xq + (int64_t)tok * a.x_stride_q)[c];
   }
-  for (int idx = tid; idx < P * (K / 32); idx += blockDim.x) {
+  for (int idx = tid; idx < PS * (K / 32); idx += blockDim.x) {
     const int sp = idx / (K / 32), c = idx % (K / 32);
-    const int tok = a.sorted[sp] / a.k;
+    const int pr = a.sorted[sp], tok = pr < P ? pr / a.k : pr - P;
     a.gd[(int64_t)sp * (K / 32) + c] = a.xd[(int64_t)tok * a.x_stride_s + c];
     a.gs[(int64_t)sp * (K / 32) + c] = a.xs[(int64_t)tok * a.x_stride_s + c];
   }
@@ -215,7 +216,7 @@ __global__ void __launch_bounds__(1024) moe_align_kernel(MoeAlignArgs a) {
 }
 
 void moe_align_launch(const MoeAlignArgs& a, cudaStream_t s, bool pdl) {
-  if (a.E > 1024) throw std::runtime_error("moe_align: E <= 1024");
+  if (a.E + (a.shared ? 1 : 0) > 1024) throw std::runtime_error("moe_align: E <= 1024 (1023 with a shared expert)");
   if (a.K % 32) throw std::runtime_error("moe_align: K must be a multiple of 32");
   launch(moe_align_kernel, dim3(1), dim3(1024), 0, s, pdl, a);
 }

@@ -89,9 +89,16 @@ def random_deepseek_weights(cfg: ModelConfig, device, seed: int = 0, std: float 
         L = DSLayer(dense, ones(H), ones(cfg.q_lora_rank), ones(LAT), ones(H),
                     w_uk=(torch.randn(nh, nope, LAT, generator=g, device=device) * std).bfloat16(),
                     w_uv=(torch.randn(nh, vd, LAT, generator=g, device=device) * std).bfloat16())
-        L.idx["qa"] = add(cfg.q_lora_rank, H)
+        # q_a and kv_a read the same normed hidden: one [q_lora + 576, H] matrix (one GEMV), with
+        # row views for each part
+        qakva = MixedWeight.random_fp8(cfg.q_lora_rank + LAT + ROPE, H, std, g, device)
+        L.idx["qakva"] = len(ws)
+        ws.append(qakva)
+        L.idx["qa"] = len(ws)
+        ws.append(qakva.rows(0, cfg.q_lora_rank))
+        L.idx["kva"] = len(ws)
+        ws.append(qakva.rows(cfg.q_lora_rank, LAT + ROPE))
         L.idx["qb"] = add(nh * (nope + rd), cfg.q_lora_rank)
-        L.idx["kva"] = add(LAT + ROPE, H)
         L.idx["o"] = add(H, nh * vd)
         if dense:
             L.idx["g"] = add(cfg.ffn, H)
@@ -101,15 +108,16 @@ def random_deepseek_weights(cfg: ModelConfig, device, seed: int = 0, std: float 
             E, F = cfg.n_experts, cfg.expert_ffn
             L.router = torch.randn(E, H, generator=g, device=device) * std
             L.router_bias = torch.randn(E, generator=g, device=device) * 0.01
-            for m, (n, k) in (("eg", (F, H)), ("eu", (F, H)), ("ed", (H, F))):
-                # all experts of one matrix drawn at once, then viewed per expert
+            Fs = cfg.shared_ffn
+            for m, sm, (n, k), (ns, ks) in (("eg", "sg", (F, H), (Fs, H)), ("eu", "su", (F, H), (Fs, H)),
+                                            ("ed", "sd", (H, F), (H, Fs))):
+                # all experts of one matrix drawn at once, then viewed per expert; the shared
+                # expert's matrix follows as "expert E" (the MoE kernels run it with the routed ones)
                 stacked = MixedWeight.random_fp8(E * n, k, std, g, device)
                 L.idx[m] = len(ws)
                 for e in range(E):
                     ws.append(stacked.rows(e * n, n))
-            L.idx["sg"] = add(cfg.shared_ffn, H)
-            L.idx["su"] = add(cfg.shared_ffn, H)
-            L.idx["sd"] = add(H, cfg.shared_ffn)
+                L.idx[sm] = add(ns, ks)
         layers.append(L)
     head = add(V, H)
     emb = QWeight.quantize(torch.randn(V, H, generator=g, device=device) * std, 1)  # F16 table
@@ -134,10 +142,11 @@ class DeepSeekModel:
         self.inp = StepInputs(R, dev)
         self.x = torch.zeros(R, H, device=dev)
         self.xa = Q8Act(R, H, dev)
-        self.qa = torch.zeros(R, cfg.q_lora_rank, device=dev)
+        self.qakva = torch.zeros(R, cfg.q_lora_rank + LAT + ROPE, device=dev)
+        self.qa = self.qakva[:, :cfg.q_lora_rank]
         self.qaq = Q8Act(R, cfg.q_lora_rank, dev)
         self.q = torch.zeros(R, nh * (nope + rd), device=dev)
-        self.kva = torch.zeros(R, LAT + ROPE, device=dev)
+        self.kva = self.qakva[:, cfg.q_lora_rank:]
         self.q_lat = torch.zeros(R, nh, LAT, device=dev)
         self.q_pe = torch.zeros(R, nh, ROPE, device=dev)
         self.o_lat = torch.zeros(R, nh, LAT, device=dev)
@@ -146,13 +155,15 @@ class DeepSeekModel:
         self.rlog = torch.zeros(R, E, device=dev)
         self.ids = torch.zeros(R, k, dtype=torch.int32, device=dev)
         self.rw = torch.zeros(R, k, device=dev)
-        self.counts = torch.zeros(E, dtype=torch.int32, device=dev)
-        self.offsets = torch.zeros(E, dtype=torch.int32, device=dev)
-        self.sorted = torch.zeros(R * k, dtype=torch.int32, device=dev)
-        self.active = torch.zeros(E, dtype=torch.int32, device=dev)
+        # the shared expert runs as expert E inside the routed launches when its shape matches
+        self.fold_shared = cfg.n_experts > 0 and cfg.shared_ffn == cfg.expert_ffn
+        self.counts = torch.zeros(E + 1, dtype=torch.int32, device=dev)
+        self.offsets = torch.zeros(E + 1, dtype=torch.int32, device=dev)
+        self.sorted = torch.zeros(R * k + R, dtype=torch.int32, device=dev)
+        self.active = torch.zeros(E + 1, dtype=torch.int32, device=dev)
         self.n_active = torch.zeros(1, dtype=torch.int32, device=dev)
-        self.gx = Q8Act(R * k, H, dev)
-        self.hx = Q8Act(R * k, F, dev)
+        self.gx = Q8Act(R * k + R, H, dev)
+        self.hx = Q8Act(R * k + R, F, dev)
         self.hs = Q8Act(R, Fs, dev)
         self.logits = torch.zeros(R, cfg.vocab, device=dev)
         self.next_ids = torch.zeros(R, dtype=torch.int32, device=dev)
@@ -172,10 +183,9 @@ class DeepSeekModel:
         cfg, t, kv, inp = self.cfg, self.w.table, self.kv, self.inp
         K = kernels()
         xa = self.xa.view(rows)
-        mixed_gemv(t, L.idx["qa"], xa, self.qa[:rows])
+        mixed_gemv(t, L.idx["qakva"], xa, self.qakva[:rows])
         ops.rmsnorm_q8(self.qa[:rows], L.q_a_norm, cfg.eps, self.qaq.view(rows))
         mixed_gemv(t, L.idx["qb"], self.qaq.view(rows), self.q[:rows])
-        mixed_gemv(t, L.idx["kva"], xa, self.kva[:rows])
         ops.launches.add(4)
         K.mla_kv_append(self.kva[:rows], L.kv_a_norm, cfg.eps, inp.positions[:rows], kv.block_tables,
                         inp.row_seq[:rows], self.rope, kv.latent[l], ops.PDL)
@@ -198,20 +208,23 @@ class DeepSeekModel:
         ops.router_logits(L.router, xa, self.rlog[:rows])
         ops.moe_topk(self.rlog[:rows], L.router_bias, k, 1, cfg.n_groups, cfg.topk_groups, cfg.norm_topk,
                      cfg.routed_scale, self.ids[:rows], self.rw[:rows])
-        ops.moe_align(self.ids[:rows], E, xa, self.counts, self.offsets, self.sorted, self.gx)
+        fold = self.fold_shared and L.idx["sg"] == L.idx["eg"] + E and L.idx["su"] == L.idx["eu"] + E and \
+            L.idx["sd"] == L.idx["ed"] + E
+        ops.moe_align(self.ids[:rows], E, xa, self.counts, self.offsets, self.sorted, self.gx, shared=fold)
         K = kernels()
         ops.launches.add(3)
         K.moe_active(self.counts, self.active, self.n_active, ops.PDL)
-        na = min(E, rows * k)
+        na = min(E, rows * k) + (1 if fold else 0)
         K.moe_mixed_gemv(0, t.descs, L.idx["eg"], L.idx["eu"], F, H, k, self.counts, self.offsets, self.sorted,
                          self.active, self.n_active, na, self.gx.q, self.gx.d, self.gx.s, self.hx.q, self.hx.d,
                          self.hx.s, None, None, ops.PDL)
         K.moe_mixed_gemv(1, t.descs, L.idx["ed"], L.idx["ed"], H, F, k, self.counts, self.offsets, self.sorted,
                          self.active, self.n_active, na, self.hx.q, self.hx.d, self.hx.s, None, None, None,
-                         self.x[:rows], self.rw[:rows].reshape(-1), ops.PDL)
-        hs = self.hs.view(rows)
-        mixed_gemv_swiglu(t, L.idx["sg"], L.idx["su"], xa, hs)
-        mixed_gemv(t, L.idx["sd"], hs, self.x[:rows], residual=True)
+                         self.x[:rows], self.rw[:rows].reshape(-1), ops.PDL, rows * k)
+        if not fold:
+            hs = self.hs.view(rows)
+            mixed_gemv_swiglu(t, L.idx["sg"], L.idx["su"], xa, hs)
+            mixed_gemv(t, L.idx["sd"], hs, self.x[:rows], residual=True)
 
     def forward(self, rows: int, sample: str = "greedy", advance: bool = False):
         cfg, w, inp = self.cfg, self.w, self.inp

@@ -229,9 +229,12 @@ def moe_topk(logits, bias, k: int, scoring: int, n_groups: int, topk_groups: int
     kernels().moe_topk(logits, bias, k, scoring, n_groups, topk_groups, renorm, scale, ids, weights, PDL)
 
 
-def moe_align(ids, E: int, x: Q8Act, counts, offsets, sorted_pairs, gathered: Q8Act):
+def moe_align(ids, E: int, x: Q8Act, counts, offsets, sorted_pairs, gathered: Q8Act, shared: bool = False):
+    """Counting sort of the (token, expert) pairs by expert plus the gather of their q8 rows;
+    ``shared`` appends expert E (a shared expert) with one pair per token after the routed ones."""
     launches.add()
-    kernels().moe_align(ids, E, x.q, x.d, x.s, counts, offsets, sorted_pairs, gathered.q, gathered.d, gathered.s, PDL)
+    kernels().moe_align(ids, E, x.q, x.d, x.s, counts, offsets, sorted_pairs, gathered.q, gathered.d, gathered.s, PDL,
+                        shared)
 
 
 def moe_gemv_swiglu(w_gate: QWeight, w_up: QWeight, N: int, E: int, k: int, counts, offsets, sorted_pairs,
