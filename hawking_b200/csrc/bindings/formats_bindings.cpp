@@ -1,9 +1,13 @@
 // Bindings for the artifact formats (.gravity shards, HGRAV* mixed codecs, HQ80M15 catalog,
 // sha256, canonical JSON).
+#include <cstring>
+
 #include <pybind11/numpy.h>
 #include <pybind11/pybind11.h>
 #include <pybind11/stl.h>
 
+#include "../native/codecs.h"
+#include "../native/ggml_quant.h"
 #include "../native/gravity.h"
 #include "../native/json.h"
 #include "../native/mixed.h"
@@ -71,6 +75,161 @@ void bind_formats(py::module_& m) {
   m.def("gravity_codec_to_ggml", &gravity_codec_to_ggml);
 
   // mixed codecs
+  // fixed-header codecs (PQ, residual PQ, AAP, HQ30 family) and the .hawking sidecar
+  using U8 = py::array_t<uint8_t, py::array::c_style>;
+  using F32 = py::array_t<float, py::array::c_style | py::array::forcecast>;
+  auto f32_np = [](const std::vector<float>& v, py::ssize_t rows, py::ssize_t cols) {
+    py::array_t<float> out({rows, cols});
+    std::memcpy(out.mutable_data(), v.data(), v.size() * 4);
+    return out;
+  };
+  auto f64_np = [](const std::vector<double>& v) {
+    py::array_t<double> out((py::ssize_t)v.size());
+    std::memcpy(out.mutable_data(), v.data(), v.size() * 8);
+    return out;
+  };
+  m.def("pq_header", [](U8 a) {
+    auto h = pq_parse(a.data(), a.size());
+    py::dict d;
+    d["d"] = h.d; d["s"] = h.s; d["sub"] = h.sub; d["card"] = h.card; d["rows"] = h.rows; d["cols"] = h.cols;
+    d["nchunk"] = h.nchunk; d["seed"] = h.seed; d["bits"] = h.bits; d["rotate"] = h.rotate;
+    d["n_codebooks"] = h.n_codebooks;
+    return d;
+  });
+  m.def("pq_parts", [](U8 a) {  // codebooks [s, card, sub] f32 and indices [rows, nchunk, s]
+    PqHeader h;
+    std::vector<float> cb;
+    std::vector<uint16_t> idx;
+    pq_sections(a.data(), a.size(), h, cb, idx);
+    py::array_t<float> c({(py::ssize_t)h.s, (py::ssize_t)h.card, (py::ssize_t)h.sub});
+    std::memcpy(c.mutable_data(), cb.data(), cb.size() * 4);
+    py::array_t<int16_t> i({(py::ssize_t)h.rows, (py::ssize_t)h.nchunk, (py::ssize_t)h.s});
+    std::memcpy(i.mutable_data(), idx.data(), idx.size() * 2);
+    return py::make_tuple(c, i);
+  });
+  m.def("pq_decode", [f32_np](U8 a) {
+    auto h = pq_parse(a.data(), a.size());
+    return f32_np(pq_decode(a.data(), a.size()), h.rows, h.cols);
+  });
+  m.def("pq_matvec_f64", [f64_np](U8 a, F32 x) { return f64_np(pq_matvec_f64(a.data(), a.size(), x.data())); });
+  m.def("pq_encode", [](int d, int s, int sub, int card, int rows, int cols, int nchunk, int seed, int bits,
+                        py::array_t<uint16_t, py::array::c_style | py::array::forcecast> cb,
+                        py::array_t<uint32_t, py::array::c_style | py::array::forcecast> idx) {
+    PqHeader h;
+    h.d = d; h.s = s; h.sub = sub; h.card = card; h.rows = rows; h.cols = cols; h.nchunk = nchunk; h.seed = seed;
+    h.bits = bits; h.rotate = 0; h.n_codebooks = (uint8_t)s;
+    return to_np(pq_encode(h, std::vector<uint16_t>(cb.data(), cb.data() + cb.size()),
+                           std::vector<uint32_t>(idx.data(), idx.data() + idx.size())));
+  });
+  m.def("rpq_header", [](U8 a) {
+    auto h = rpq_parse(a.data(), a.size());
+    py::dict d;
+    d["d"] = h.d; d["stages"] = h.stages; d["card"] = h.card; d["rows"] = h.rows; d["cols"] = h.cols;
+    d["nchunk"] = h.nchunk; d["seed"] = h.seed; d["bits"] = h.bits;
+    return d;
+  });
+  m.def("rpq_parts", [](U8 a) {  // codebooks [stages, card, d] f32 and indices [rows, nchunk, stages]
+    RpqHeader h;
+    std::vector<float> cb;
+    std::vector<uint16_t> idx;
+    rpq_sections(a.data(), a.size(), h, cb, idx);
+    py::array_t<float> c({(py::ssize_t)h.stages, (py::ssize_t)h.card, (py::ssize_t)h.d});
+    std::memcpy(c.mutable_data(), cb.data(), cb.size() * 4);
+    py::array_t<int16_t> i({(py::ssize_t)h.rows, (py::ssize_t)h.nchunk, (py::ssize_t)h.stages});
+    std::memcpy(i.mutable_data(), idx.data(), idx.size() * 2);
+    return py::make_tuple(c, i);
+  });
+  m.def("rpq_decode", [f32_np](U8 a) {
+    auto h = rpq_parse(a.data(), a.size());
+    return f32_np(rpq_decode(a.data(), a.size()), h.rows, h.cols);
+  });
+  m.def("rpq_matvec_f64", [f64_np](U8 a, F32 x) { return f64_np(rpq_matvec_f64(a.data(), a.size(), x.data())); });
+  m.def("rpq_encode", [](int d, int stages, int card, int rows, int cols, int nchunk, int seed, int bits,
+                         py::array_t<uint16_t, py::array::c_style | py::array::forcecast> cb,
+                         py::array_t<uint32_t, py::array::c_style | py::array::forcecast> idx) {
+    RpqHeader h;
+    h.d = d; h.stages = stages; h.card = card; h.rows = rows; h.cols = cols; h.nchunk = nchunk; h.seed = seed;
+    h.bits = bits;
+    return to_np(rpq_encode(h, std::vector<uint16_t>(cb.data(), cb.data() + cb.size()),
+                            std::vector<uint32_t>(idx.data(), idx.data() + idx.size())));
+  });
+  m.def("aap_header", [](U8 a) {
+    auto h = aap_parse(a.data(), a.size());
+    py::dict d;
+    d["rows"] = h.rows; d["cols"] = h.cols; d["rank"] = h.rank; d["basis_layer"] = h.basis_layer;
+    d["side"] = h.side == 1 ? "input" : "output"; d["has_basis"] = h.has_basis;
+    return d;
+  });
+  m.def("aap_decode", [f32_np](U8 a) {
+    auto h = aap_parse(a.data(), a.size());
+    return f32_np(aap_decode(a.data(), a.size()), h.rows, h.cols);
+  });
+  m.def("aap_matvec_f64", [f64_np](U8 a, F32 x) { return f64_np(aap_matvec_f64(a.data(), a.size(), x.data())); });
+  m.def("aap_encode", [](int rows, int cols, int rank, int basis_layer, int side,
+                         py::array_t<uint16_t, py::array::c_style | py::array::forcecast> coeff,
+                         py::array_t<uint16_t, py::array::c_style | py::array::forcecast> basis) {
+    AapHeader h;
+    h.rows = rows; h.cols = cols; h.rank = rank; h.basis_layer = basis_layer; h.side = side; h.has_basis = true;
+    return to_np(aap_encode(h, std::vector<uint16_t>(coeff.data(), coeff.data() + coeff.size()),
+                            std::vector<uint16_t>(basis.data(), basis.data() + basis.size())));
+  });
+  auto hq30_dict = [](const Hq30Header& h) {
+    py::dict d;
+    d["version"] = h.version; d["group_size"] = h.group_size; d["shape"] = h.shape; d["elements"] = h.elements;
+    d["groups"] = h.groups; d["scale_offset"] = h.scale_offset; d["code_offset"] = h.code_offset;
+    d["payload_bytes"] = h.payload_bytes;
+    return d;
+  };
+  m.def("hq30_binary_header", [hq30_dict](U8 a) { return hq30_dict(hq30_binary_parse(a.data(), a.size())); });
+  m.def("hq30_uq4_header", [hq30_dict](U8 a) { return hq30_dict(hq30_uq4_parse(a.data(), a.size())); });
+  m.def("hq30_residual_header", [hq30_dict](U8 a) {
+    auto r = hq30_residual_parse(a.data(), a.size());
+    py::dict d = hq30_dict(r.base);
+    d["base_offset"] = r.base_offset; d["base_bytes"] = r.base_bytes; d["indices"] = r.indices;
+    std::vector<float> vals;
+    for (uint16_t v : r.values) vals.push_back(fp16_to_f32(v));
+    d["values"] = vals;
+    return d;
+  });
+  auto flat_np = [](const std::vector<float>& v) {
+    py::array_t<float> out((py::ssize_t)v.size());
+    std::memcpy(out.mutable_data(), v.data(), v.size() * 4);
+    return out;
+  };
+  m.def("hq30_binary_decode", [flat_np](U8 a) { return flat_np(hq30_binary_decode(a.data(), a.size())); });
+  m.def("hq30_uq4_decode", [flat_np](U8 a) { return flat_np(hq30_uq4_decode(a.data(), a.size())); });
+  m.def("hq30_residual_decode", [flat_np](U8 a) { return flat_np(hq30_residual_decode(a.data(), a.size())); });
+  m.def("hq30_binary_encode", [](std::vector<uint32_t> shape, F32 w, int group) {
+    return to_np(hq30_binary_encode(shape, w.data(), group));
+  });
+  m.def("hq30_uq4_encode", [](std::vector<uint32_t> shape, F32 w, int group) {
+    return to_np(hq30_uq4_encode(shape, w.data(), group));
+  });
+  m.def("hq30_residual_encode", [](std::vector<uint32_t> shape, F32 w, int group, size_t keep) {
+    return to_np(hq30_residual_encode(shape, w.data(), group, keep));
+  });
+  m.def("predecode_q4k_scales", [flat_np](U8 a) { return flat_np(predecode_q4k_scales(a.data(), a.size())); });
+  m.def("sidecar_write", [](const std::string& path, const std::string& header_json, py::list entries) {
+    std::vector<SidecarEntry> es;
+    for (auto item : entries) {
+      auto t = item.cast<py::tuple>();
+      SidecarEntry e;
+      e.offset = t[0].cast<uint64_t>();
+      auto arr = t[1].cast<py::array_t<float, py::array::c_style | py::array::forcecast>>();
+      e.scales.assign(arr.data(), arr.data() + arr.size());
+      es.push_back(std::move(e));
+    }
+    sidecar_write(path, header_json, es);
+  });
+  m.def("sidecar_read", [flat_np](const std::string& path) {
+    std::string hj;
+    std::vector<SidecarEntry> es;
+    sidecar_read(path, hj, es);
+    py::list out;
+    for (auto& e : es) out.append(py::make_tuple(e.offset, flat_np(e.scales)));
+    return py::make_tuple(hj, out);
+  });
+
   m.def("mixed_header", [](py::array_t<uint8_t, py::array::c_style> a) {
     auto e = mixed_split(a.data(), a.size());
     return py::make_tuple(py::bytes(e.magic), to_py(e.header), (size_t)(e.body - a.data()), e.body_bytes);

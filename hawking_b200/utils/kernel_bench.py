@@ -11,6 +11,8 @@ form to put under a profiler (few launches, small device footprint).
 
     python -m hawking_b200.utils.kernel_bench                       # all cases, timed
     python -m hawking_b200.utils.kernel_bench --case down --plain   # one case, 3 eager launches
+    python -m hawking_b200.utils.kernel_bench --rows 64 --case tc_gate_up --case tc_down   # tensor cores
+    python -m hawking_b200.utils.kernel_bench --rows 2048 --case attention_prefill
 """
 from __future__ import annotations
 
@@ -63,6 +65,8 @@ def build_cases(dev: str = "cuda", ctx: int = 2048, rows: int = 1, only=None):
         return [[w(n, k) for n, k in shape_list] for _ in range(reps)]
 
     cases = {}
+    if only is not None and all(c.startswith("tc_") or c == "attention_prefill" for c in only):
+        return _tc_cases(dev, ctx, rows, g, only)
     wo, wd, wqkv, wgu = copies((H, H)), copies((H, F)), copies((6144, H)), copies((F, H), (F, H))
     x = torch.randn(rows, H, device=dev)
     nw = torch.ones(H, device=dev)
@@ -113,6 +117,41 @@ def build_cases(dev: str = "cuda", ctx: int = 2048, rows: int = 1, only=None):
     return cases
 
 
+def _tc_cases(dev, ctx, rows, g, only):
+    """Tensor-core cases at ``rows`` tokens: the Q4_K dequant GEMMs of one layer and the causal
+    prefill attention of one ``rows``-token chunk at the end of a ``ctx``-token prompt."""
+    from hawking_b200 import ops
+    from hawking_b200.formats.ggml import GgmlType
+    from hawking_b200.ops import QWeight
+
+    cases = {}
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    x = torch.randn(rows, F, device=dev).bfloat16()
+    for name, (n, k) in (("tc_gate_up", (2 * F, H)), ("tc_down", (H, F)), ("tc_qkv", (6144, H)),
+                         ("tc_o", (H, H))):
+        if name not in only:
+            continue
+        one = n * k * 144 // 256
+        ws = [QWeight.random(GgmlType.Q4_K, n, k, 0.02, g, dev) for _ in range(max(1, -(-(256 << 20) // one)))]
+        y = torch.zeros(rows, n, device=dev)
+        cases[name] = (lambda i, ws=ws, y=y, k=k: ops.tc_gemm(ws[i % len(ws)], x[:, :k], y, status, atomic=True),
+                       one, 2.0 * rows * n * k)
+    if "attention_prefill" in only:
+        nblk = (ctx + BS - 1) // BS
+        kc = torch.randn(nblk, NKV, BS, HD, device=dev).bfloat16()
+        vc = torch.randn_like(kc)
+        tables = torch.arange(nblk, dtype=torch.int32, device=dev).view(1, nblk).contiguous()
+        rs = torch.zeros(rows, dtype=torch.int32, device=dev)
+        rc = torch.arange(ctx - rows + 1, ctx + 1, dtype=torch.int32, device=dev)
+        q = torch.randn(rows, NH, HD, device=dev)
+        ob = torch.zeros(rows, NH * HD, dtype=torch.bfloat16, device=dev)
+        keys = float(rc.sum().item())  # causal keys summed over the rows
+        cases["attention_prefill"] = (
+            lambda i: ops.attention_prefill(q, kc, vc, tables, rs, rc, HD ** -0.5, out_bf16=ob),
+            ctx * NKV * HD * 2 * 2, 4.0 * keys * NH * HD)
+    return cases
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--case", action="append", help="case name (repeatable); default all")
@@ -124,7 +163,8 @@ def main(argv=None) -> None:
     cases = build_cases(ctx=args.ctx, rows=args.rows, only=args.case)
     names = args.case or list(cases)
     for n in names:
-        fn, nbytes = cases[n]
+        fn, nbytes = cases[n][:2]
+        flops = cases[n][2] if len(cases[n]) > 2 else None
         if args.plain:
             for i in range(3):
                 fn(i)
@@ -132,8 +172,11 @@ def main(argv=None) -> None:
             print(json.dumps({"case": n, "plain": True}))
             continue
         us = _time_graph(fn, args.iters)
-        print(json.dumps({"case": n, "rows": args.rows, "us": round(us, 3),
-                          "gb_s": round(nbytes / us / 1e3, 1), "bytes": int(nbytes)}), flush=True)
+        rec = {"case": n, "rows": args.rows, "us": round(us, 3), "gb_s": round(nbytes / us / 1e3, 1),
+               "bytes": int(nbytes)}
+        if flops:
+            rec["tflops"] = round(flops / us / 1e6, 1)
+        print(json.dumps(rec), flush=True)
 
 
 if __name__ == "__main__":
