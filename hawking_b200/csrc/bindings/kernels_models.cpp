@@ -24,7 +24,8 @@ template <typename T> T* optr(const optional<Tensor>& t) { return t.has_value() 
 
 // Pack descriptors (codes / scales tensors + codec fields) into a device byte tensor.
 Tensor mixed_descs(const std::vector<Tensor>& codes, const std::vector<Tensor>& scales, const std::vector<int64_t>& kind,
-                   const std::vector<int64_t>& bits, const std::vector<int64_t>& group) {
+                   const std::vector<int64_t>& bits, const std::vector<int64_t>& group,
+                   const std::vector<int64_t>& zeros) {
   const size_t n = codes.size();
   TORCH_CHECK(scales.size() == n && kind.size() == n && bits.size() == n && group.size() == n, "mixed_descs: lengths");
   std::vector<hk::MixedDesc> h(n);
@@ -43,7 +44,10 @@ Tensor mixed_descs(const std::vector<Tensor>& codes, const std::vector<Tensor>& 
     h[i].kind = (int)kind[i];
     h[i].bits = (int)bits[i];
     h[i].group = (int)group[i];
-    h[i].bound = kind[i] == hk::MIXED_UNIFORM ? (1 << (bits[i] - 1)) - 1 : 0;
+    // the code's zero point: 2^(bits-1) - 1 for HGRAVU01; HQ30UQ4 stores q + 8 (zero 8)
+    h[i].bound = kind[i] == hk::MIXED_UNIFORM ? (i < zeros.size() && zeros[i] >= 0 ? (int)zeros[i]
+                                                                                    : (1 << (bits[i] - 1)) - 1)
+                                              : 0;
     TORCH_CHECK(kind[i] == hk::MIXED_BINARY ? bits[i] == 1
                                             : (kind[i] == hk::MIXED_FP8 ? bits[i] == 8
                                                                         : (bits[i] == 2 || bits[i] == 4 || bits[i] == 8)),
@@ -134,6 +138,73 @@ void moe_mixed_gemv(int64_t epi, const Tensor& descs, int64_t base0, int64_t bas
   TORCH_CHECK(epi == 0 ? a.oq != nullptr : (a.y != nullptr && a.route_w != nullptr), "moe_mixed_gemv: outputs");
   const c10::cuda::CUDAGuard g(xq.device());
   hk::moe_mixed_gemv_launch((int)epi, a, (int)max_active, cur_stream(), pdl);
+}
+
+void codebook_gemv(const Tensor& codebooks, const Tensor& codes, int64_t rows, int64_t nchunk, int64_t nsub,
+                   int64_t card, int64_t width, int64_t d, int64_t sub_stride, int64_t bits, const Tensor& xq,
+                   const Tensor& xd, const Tensor& lut, const Tensor& y, double alpha, bool accumulate, bool pdl) {
+  TORCH_CHECK(codebooks.is_cuda() && codebooks.scalar_type() == at::kHalf, "codebook gemv: fp16 codebooks");
+  TORCH_CHECK(codes.is_cuda() && codes.scalar_type() == at::kByte, "codebook gemv: uint8 code stream");
+  const int64_t need_bits = rows * nchunk * nsub * bits;
+  TORCH_CHECK(codes.numel() >= (need_bits + 7) / 8 + 4, "codebook gemv: code stream too short (needs 4 bytes padding)");
+  TORCH_CHECK(codebooks.numel() == nsub * card * width, "codebook gemv: codebook size");
+  const int nb = (int)xq.size(0);
+  TORCH_CHECK(lut.scalar_type() == at::kFloat && lut.numel() >= nb * nchunk * nsub * card, "codebook gemv: LUT scratch");
+  TORCH_CHECK(y.scalar_type() == at::kFloat && y.size(0) >= nb && y.size(1) >= rows && y.stride(1) == 1, "codebook gemv: y");
+  TORCH_CHECK(xq.size(1) >= (nchunk - 1) * d + (nsub - 1) * sub_stride + width, "codebook gemv: activation width");
+  hk::CodebookArgs a{};
+  a.codebooks = ptr<__half>(codebooks);
+  a.codes = ptr<uint8_t>(codes);
+  a.rows = (int)rows; a.nchunk = (int)nchunk; a.nsub = (int)nsub; a.card = (int)card; a.width = (int)width;
+  a.d = (int)d; a.sub_stride = (int)sub_stride; a.bits = (int)bits;
+  a.xq = ptr<int8_t>(xq); a.xd = ptr<float>(xd);
+  a.x_stride_q = xq.stride(0); a.x_stride_s = xd.stride(0);
+  a.nb = nb;
+  a.lut = ptr<float>(lut);
+  a.y = ptr<float>(y); a.y_stride = y.stride(0);
+  a.alpha = (float)alpha;
+  a.accumulate = accumulate ? 1 : 0;
+  const c10::cuda::CUDAGuard g(xq.device());
+  hk::codebook_gemv_launch(a, cur_stream(), pdl);
+}
+
+void aap_gemv(const Tensor& in_proj, const Tensor& out_proj, int64_t rows, int64_t cols, int64_t rank, int64_t side,
+              const Tensor& xq, const Tensor& xd, const Tensor& latent, const Tensor& y, double alpha, bool accumulate,
+              bool pdl) {
+  TORCH_CHECK(in_proj.scalar_type() == at::kHalf && out_proj.scalar_type() == at::kHalf, "aap gemv: fp16 factors");
+  TORCH_CHECK(in_proj.numel() == cols * rank && out_proj.numel() == rows * rank, "aap gemv: factor sizes");
+  TORCH_CHECK(side == 1 || side == 2, "aap gemv: side 1 (input) or 2 (output)");
+  const int nb = (int)xq.size(0);
+  TORCH_CHECK(latent.scalar_type() == at::kFloat && latent.numel() >= nb * rank, "aap gemv: latent scratch");
+  TORCH_CHECK(y.scalar_type() == at::kFloat && y.size(0) >= nb && y.size(1) >= rows && y.stride(1) == 1, "aap gemv: y");
+  hk::AapArgs a{};
+  a.in_proj = ptr<__half>(in_proj); a.out_proj = ptr<__half>(out_proj);
+  a.rows = (int)rows; a.cols = (int)cols; a.rank = (int)rank; a.side = (int)side;
+  a.xq = ptr<int8_t>(xq); a.xd = ptr<float>(xd);
+  a.x_stride_q = xq.stride(0); a.x_stride_s = xd.stride(0);
+  a.nb = nb;
+  a.latent = ptr<float>(latent);
+  a.y = ptr<float>(y); a.y_stride = y.stride(0);
+  a.alpha = (float)alpha;
+  a.accumulate = accumulate ? 1 : 0;
+  const c10::cuda::CUDAGuard g(xq.device());
+  hk::aap_gemv_launch(a, cur_stream(), pdl);
+}
+
+void sparse_rows(const Tensor& row_ptr, const Tensor& col, const Tensor& val, const Tensor& xq, const Tensor& xd,
+                 const Tensor& y, double alpha, bool pdl) {
+  TORCH_CHECK(row_ptr.scalar_type() == at::kInt && col.scalar_type() == at::kInt && val.scalar_type() == at::kHalf,
+              "sparse rows: int32 row_ptr / col, fp16 values");
+  hk::SparseArgs a{};
+  a.row_ptr = ptr<int>(row_ptr); a.col = ptr<int>(col); a.val = ptr<__half>(val);
+  a.rows = (int)row_ptr.numel() - 1;
+  a.xq = ptr<int8_t>(xq); a.xd = ptr<float>(xd);
+  a.x_stride_q = xq.stride(0); a.x_stride_s = xd.stride(0);
+  a.nb = (int)xq.size(0);
+  a.y = ptr<float>(y); a.y_stride = y.stride(0);
+  a.alpha = (float)alpha;
+  const c10::cuda::CUDAGuard g(xq.device());
+  hk::sparse_rows_launch(a, cur_stream(), pdl);
 }
 
 void deltanet_conv(const Tensor& qkvz, const Tensor& conv_w, const Tensor& conv_state, const optional<Tensor>& slot,
@@ -274,7 +345,17 @@ void register_model_kernels(py::module_& m) {
         py::arg("status"), py::arg("pdl") = false);
   m.def("mla_out", &mla_out, py::arg("o_lat"), py::arg("w_uv"), py::arg("oq"), py::arg("od"), py::arg("os"),
         py::arg("pdl") = false);
-  m.def("mixed_descs", &mixed_descs);
+  m.def("mixed_descs", &mixed_descs, py::arg("codes"), py::arg("scales"), py::arg("kind"), py::arg("bits"),
+        py::arg("group"), py::arg("zeros") = std::vector<int64_t>{});
+  m.def("codebook_gemv", &codebook_gemv, py::arg("codebooks"), py::arg("codes"), py::arg("rows"), py::arg("nchunk"),
+        py::arg("nsub"), py::arg("card"), py::arg("width"), py::arg("d"), py::arg("sub_stride"), py::arg("bits"),
+        py::arg("xq"), py::arg("xd"), py::arg("lut"), py::arg("y"), py::arg("alpha") = 1.0,
+        py::arg("accumulate") = false, py::arg("pdl") = false);
+  m.def("aap_gemv", &aap_gemv, py::arg("in_proj"), py::arg("out_proj"), py::arg("rows"), py::arg("cols"),
+        py::arg("rank"), py::arg("side"), py::arg("xq"), py::arg("xd"), py::arg("latent"), py::arg("y"),
+        py::arg("alpha") = 1.0, py::arg("accumulate") = false, py::arg("pdl") = false);
+  m.def("sparse_rows", &sparse_rows, py::arg("row_ptr"), py::arg("col"), py::arg("val"), py::arg("xq"),
+        py::arg("xd"), py::arg("y"), py::arg("alpha") = 1.0, py::arg("pdl") = false);
   m.def("mixed_gemv", &mixed_gemv, py::arg("epi"), py::arg("descs"), py::arg("d0"), py::arg("d1"), py::arg("N"),
         py::arg("K"), py::arg("xq"), py::arg("xd"), py::arg("xs"), py::arg("y") = py::none(), py::arg("alpha") = 1.0,
         py::arg("oq") = py::none(), py::arg("od") = py::none(), py::arg("os") = py::none(), py::arg("pdl") = false,

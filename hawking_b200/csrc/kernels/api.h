@@ -321,6 +321,52 @@ struct MoeMixedArgs {
 void moe_mixed_gemv_launch(int epi, const MoeMixedArgs& a, int max_active, cudaStream_t s, bool pdl);
 void moe_active_launch(const int* counts, int E, int* active, int* n_active, cudaStream_t s, bool pdl);
 
+// ---- codebook / low-rank / sparse GEMVs (codebook.cu) ----
+struct CodebookArgs {
+  const __half* codebooks;    // [nsub][card][width]
+  const uint8_t* codes;       // MSB-first packed indices [rows][nchunk][nsub] (+4 bytes padding)
+  int rows, nchunk, nsub, card, width, d, sub_stride, bits;
+  const int8_t* xq;           // q8 activations [nb, cols]
+  const float* xd;
+  int64_t x_stride_q, x_stride_s;
+  int nb;
+  float* lut;                 // scratch [nb][nchunk * nsub * card]
+  float* y;                   // [nb, y_stride]
+  int64_t y_stride;
+  float alpha;
+  int accumulate;
+};
+void codebook_gemv_launch(const CodebookArgs& a, cudaStream_t s, bool pdl);
+struct AapArgs {
+  const __half* in_proj;      // input side: basis [cols, rank]; output side: coefficients [rank, cols]
+  const __half* out_proj;     // [rows, rank]: coefficients (input side) or basis (output side)
+  int rows, cols, rank, side;
+  const int8_t* xq;
+  const float* xd;
+  int64_t x_stride_q, x_stride_s;
+  int nb;
+  float* latent;              // scratch [nb, rank]
+  float* y;
+  int64_t y_stride;
+  float alpha;
+  int accumulate;
+};
+void aap_gemv_launch(const AapArgs& a, cudaStream_t s, bool pdl);
+struct SparseArgs {           // y[b][r] += alpha * sum over row r's entries of val * x_b[col]
+  const int* row_ptr;         // [rows + 1]
+  const int* col;
+  const __half* val;
+  int rows;
+  const int8_t* xq;
+  const float* xd;
+  int64_t x_stride_q, x_stride_s;
+  int nb;
+  float* y;
+  int64_t y_stride;
+  float alpha;
+};
+void sparse_rows_launch(const SparseArgs& a, cudaStream_t s, bool pdl);
+
 // ---- gated DeltaNet (deltanet.cu) ----
 struct DeltaConvArgs {
   const float* qkvz;          // [R, qkvz_stride] fused projection (per key head: q k v z)

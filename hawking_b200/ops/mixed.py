@@ -47,10 +47,13 @@ class MixedWeight:
     K: int
     codes: torch.Tensor   # uint8 [N, K * bits / 8]
     scales: torch.Tensor  # fp16 [N, K / group]
+    zero: int = -1        # uniform code zero point; -1 = 2^(bits-1) - 1 (HGRAVU01), 8 for HQ30UQ4
 
     @property
     def bound(self) -> int:
-        return (1 << (self.bits - 1)) - 1 if self.kind == UNIFORM else 0
+        if self.kind != UNIFORM:
+            return 0
+        return self.zero if self.zero >= 0 else (1 << (self.bits - 1)) - 1
 
     @property
     def nbytes(self) -> int:
@@ -156,7 +159,30 @@ class MixedWeight:
 
     def rows(self, start: int, count: int) -> "MixedWeight":
         return MixedWeight(self.kind, self.bits, self.group, count, self.K, self.codes[start:start + count],
-                           self.scales[start:start + count])
+                           self.scales[start:start + count], self.zero)
+
+    @staticmethod
+    def from_hq30(payload: np.ndarray, device) -> "MixedWeight":
+        """A 2-D HQ30G1B1 (binary) or HQ30UQ4 (4-bit, zero point 8) payload whose groups tile the
+        rows: the body maps onto the device layout as is (scales [N, K / group], codes LSB-first)."""
+        from ..formats import codecs
+        payload = np.ascontiguousarray(payload, dtype=np.uint8)
+        k = codecs.kind(payload)
+        h = codecs.header(payload)
+        if k not in ("complete_binary", "uniform_q4") or len(h["shape"]) != 2:
+            raise ValueError("from_hq30: a rank-2 HQ30G1B1 or HQ30UQ4 payload")
+        rows, cols = h["shape"]
+        gs = h["group_size"]
+        if cols % gs or gs % 32:
+            raise ValueError("from_hq30: groups must tile the rows (cols % group == 0, group % 32 == 0)")
+        so, co = h["scale_offset"], h["code_offset"]
+        scales = torch.from_numpy(payload[so:co].copy().view(np.float16).reshape(rows, cols // gs))
+        if k == "complete_binary":
+            codes = torch.from_numpy(payload[co:].copy().reshape(rows, cols // 8))
+            return MixedWeight(BINARY, 1, gs, rows, cols, codes.to(device).contiguous(), scales.to(device).contiguous())
+        codes = torch.from_numpy(payload[co:].copy().reshape(rows, cols // 2))
+        return MixedWeight(UNIFORM, 4, gs, rows, cols, codes.to(device).contiguous(), scales.to(device).contiguous(),
+                           zero=8)
 
 
 class MixedTable:
@@ -166,7 +192,7 @@ class MixedTable:
         self.weights = list(weights)
         self.descs = kernels().mixed_descs([w.codes for w in weights], [w.scales for w in weights],
                                            [w.kind for w in weights], [w.bits for w in weights],
-                                           [w.group for w in weights])
+                                           [w.group for w in weights], [w.zero for w in weights])
 
     @property
     def nbytes(self) -> int:
