@@ -110,9 +110,14 @@ void moe_mixed_gemv(int64_t epi, const Tensor& descs, int64_t base0, int64_t bas
                     const Tensor& counts, const Tensor& offsets, const Tensor& sorted, const Tensor& active,
                     const Tensor& n_active, int64_t max_active, const Tensor& xq, const Tensor& xd, const Tensor& xs,
                     const optional<Tensor>& oq, const optional<Tensor>& od, const optional<Tensor>& os,
-                    const optional<Tensor>& y, const optional<Tensor>& route_w, bool pdl, int64_t routed_pairs) {
+                    const optional<Tensor>& y, const optional<Tensor>& route_w, bool pdl, int64_t routed_pairs,
+                    bool direct) {
   hk::MoeMixedArgs a{};
   a.routed_pairs = routed_pairs < 0 ? INT_MAX : (int)routed_pairs;
+  a.direct = direct ? 1 : 0;
+  a.x_stride_q = xq.stride(0);
+  a.x_stride_s = xd.stride(0);
+  TORCH_CHECK(!direct || routed_pairs >= 0, "moe_mixed_gemv: direct input needs routed_pairs");
   a.desc = reinterpret_cast<const hk::MixedDesc*>(descs.data_ptr());
   a.desc_base0 = (int)base0;
   a.desc_base1 = (int)base1;
@@ -366,7 +371,8 @@ void register_model_kernels(py::module_& m) {
         py::arg("active"), py::arg("n_active"), py::arg("max_active"), py::arg("xq"), py::arg("xd"), py::arg("xs"),
         py::arg("oq") = py::none(), py::arg("od") = py::none(), py::arg("os") = py::none(), py::arg("y") = py::none(),
         py::arg("route_w") = py::none(), py::arg("pdl") = false,
-        py::arg("routed_pairs") = -1);
+        py::arg("routed_pairs") = -1,
+        py::arg("direct") = false);
   m.def("deltanet_conv", &deltanet_conv, py::arg("qkvz"), py::arg("conv_w"), py::arg("conv_state"), py::arg("slot"),
         py::arg("kh"), py::arg("r"), py::arg("dk"), py::arg("dv"), py::arg("kc"), py::arg("eps"), py::arg("q"),
         py::arg("k"), py::arg("v"), py::arg("z"), py::arg("pdl") = false);

@@ -101,6 +101,48 @@ void moe_topk(const Tensor& logits, const c10::optional<Tensor>& bias, int64_t k
   hk::moe_topk_launch(a, cur_stream(), pdl);
 }
 
+void moe_route(const Tensor& router, const Tensor& xq, const Tensor& xd, int64_t k, int64_t scoring,
+               const c10::optional<Tensor>& bias, int64_t n_groups, int64_t topk_groups, bool renorm, double scale,
+               const Tensor& logits, const Tensor& ids, const Tensor& weights, const Tensor& counts,
+               const Tensor& offsets, const Tensor& sorted, const Tensor& active, const Tensor& n_active, bool shared,
+               const Tensor& counter, bool pdl) {
+  TORCH_CHECK(router.scalar_type() == at::kFloat && router.dim() == 2, "moe_route: fp32 router [E, K]");
+  hk::MoeRouteArgs a{};
+  a.router = router.data_ptr<float>();
+  a.E = (int)router.size(0);
+  a.K = (int)router.size(1);
+  a.T = (int)xq.size(0);
+  TORCH_CHECK(xq.size(1) >= a.K, "moe_route: activation width");
+  a.xq = xq.data_ptr<int8_t>();
+  a.xd = xd.data_ptr<float>();
+  a.x_stride_q = xq.stride(0);
+  a.x_stride_s = xd.stride(0);
+  a.k = (int)k;
+  a.bias = bias.has_value() ? bias->data_ptr<float>() : nullptr;
+  a.scoring = (int)scoring;
+  a.n_groups = (int)n_groups;
+  a.topk_groups = (int)topk_groups;
+  a.renorm = renorm;
+  a.scale = (float)scale;
+  TORCH_CHECK(logits.numel() >= (int64_t)a.T * a.E && ids.numel() >= (int64_t)a.T * a.k &&
+                  weights.numel() >= (int64_t)a.T * a.k, "moe_route: logits / ids / weights too small");
+  TORCH_CHECK(counts.numel() >= a.E + (shared ? 1 : 0) && offsets.numel() >= a.E + (shared ? 1 : 0) &&
+                  active.numel() >= a.E + (shared ? 1 : 0) && sorted.numel() >= (int64_t)a.T * a.k + (shared ? a.T : 0),
+              "moe_route: routing buffers too small");
+  a.logits = logits.data_ptr<float>();
+  a.ids = ids.data_ptr<int>();
+  a.weights = weights.data_ptr<float>();
+  a.counts = counts.data_ptr<int>();
+  a.offsets = offsets.data_ptr<int>();
+  a.sorted = sorted.data_ptr<int>();
+  a.active = active.data_ptr<int>();
+  a.n_active = n_active.data_ptr<int>();
+  a.shared = shared ? 1 : 0;
+  a.counter = counter.data_ptr<int>();
+  const c10::cuda::CUDAGuard g(xq.device());
+  hk::moe_route_launch(a, cur_stream(), pdl);
+}
+
 void moe_align(const Tensor& ids, int64_t E, const Tensor& xq, const Tensor& xd, const Tensor& xs,
                const Tensor& counts, const Tensor& offsets, const Tensor& sorted, const Tensor& gq,
                const Tensor& gd, const Tensor& gs, bool pdl, bool shared) {
@@ -172,6 +214,11 @@ void register_more_kernels(py::module_& m) {
   m.def("moe_topk", &moe_topk, py::arg("logits"), py::arg("bias"), py::arg("k"), py::arg("scoring"),
         py::arg("n_groups"), py::arg("topk_groups"), py::arg("renorm"), py::arg("scale"), py::arg("ids"),
         py::arg("weights"), py::arg("pdl") = false);
+  m.def("moe_route", &moe_route, py::arg("router"), py::arg("xq"), py::arg("xd"), py::arg("k"), py::arg("scoring"),
+        py::arg("bias"), py::arg("n_groups"), py::arg("topk_groups"), py::arg("renorm"), py::arg("scale"),
+        py::arg("logits"), py::arg("ids"), py::arg("weights"), py::arg("counts"), py::arg("offsets"),
+        py::arg("sorted"), py::arg("active"), py::arg("n_active"), py::arg("shared"), py::arg("counter"),
+        py::arg("pdl") = false);
   m.def("moe_align", &moe_align, py::arg("ids"), py::arg("E"), py::arg("xq"), py::arg("xd"), py::arg("xs"),
         py::arg("counts"), py::arg("offsets"), py::arg("sorted"), py::arg("gq"), py::arg("gd"), py::arg("gs"),
         py::arg("pdl") = false,

@@ -233,6 +233,28 @@ struct MoeTopkArgs {
 };
 void moe_topk_launch(const MoeTopkArgs& a, cudaStream_t s, bool pdl);
 
+struct MoeRouteArgs {           // fused decode routing (moe.cu)
+  const float* router;          // [E, K] fp32
+  const int8_t* xq;             // q8 hidden [T, K]
+  const float* xd;
+  int64_t x_stride_q, x_stride_s;
+  int T, E, K, k;
+  const float* bias;
+  int scoring, n_groups, topk_groups, renorm;
+  float scale;
+  float* logits;                // scratch [T, E]
+  int* ids;                     // [T, k]
+  float* weights;               // [T, k]
+  int* counts;                  // [E + 1]
+  int* offsets;                 // [E + 1]
+  int* sorted;                  // [T * k + T]
+  int* active;                  // [E + 1]
+  int* n_active;
+  int shared;                   // append the shared expert as expert E
+  int* counter;                 // zero-initialised arrival counter (reset by the kernel)
+};
+void moe_route_launch(const MoeRouteArgs& a, cudaStream_t s, bool pdl);
+
 struct MoeAlignArgs {
   const int* ids;        // [T, k]
   int T, k, E, K;
@@ -317,6 +339,8 @@ struct MoeMixedArgs {
   const float* route_w;
   int routed_pairs;           // pairs below this are routed (token pair / k, weight route_w[pair]);
                               // the rest are shared-expert pairs (token pair - routed_pairs, weight 1)
+  int direct;                 // epi 0: read each pair's token row of xq/xd/xs (strides below)
+  int64_t x_stride_q, x_stride_s;
 };
 void moe_mixed_gemv_launch(int epi, const MoeMixedArgs& a, int max_active, cudaStream_t s, bool pdl);
 void moe_active_launch(const int* counts, int E, int* active, int* n_active, cudaStream_t s, bool pdl);

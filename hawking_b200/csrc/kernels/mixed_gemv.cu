@@ -191,6 +191,13 @@ __global__ void __launch_bounds__(256) moe_mixed_gemv_kernel(MoeMixedArgs a) {
     const int8_t* xq = a.xq + (int64_t)sp * a.K;
     const float* xd = a.xd + (int64_t)sp * (a.K / 32);
     const float* xs = a.xs + (int64_t)sp * (a.K / 32);
+    if (EPI == 0 && a.direct) {  // the pair's token row, no gathered copy
+      const int pair = a.sorted[sp];
+      const int tok = pair < a.routed_pairs ? pair / a.k : pair - a.routed_pairs;
+      xq = a.xq + (int64_t)tok * a.x_stride_q;
+      xd = a.xd + (int64_t)tok * a.x_stride_s;
+      xs = a.xs + (int64_t)tok * a.x_stride_s;
+    }
     if constexpr (EPI == 0) {
 #pragma unroll 1
       for (int r = 0; r < 4; ++r) {

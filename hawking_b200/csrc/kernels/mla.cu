@@ -70,64 +70,141 @@ void mla_kv_append_launch(const MlaAppendArgs& a, int rows, cudaStream_t s, bool
 
 // ---- q absorption: q_lat[h] = W_UK[h]^T q_nope[h]; q_pe RoPE ------------------------------------
 // Grid (heads, rows), 256 threads; W_UK is [heads, nope, 512] bf16 (row i = key dim i of head h).
-__global__ void __launch_bounds__(256) mla_absorb_q_kernel(MlaAbsorbArgs a) {
-  __shared__ float qn[256];
+// Grid (heads, 4 latent quarters); 256 threads: thread t owns 8 consecutive latent dims of the
+// quarter (t / 16) and one sixteenth of the nope rows (t % 16), with 16-byte weight loads (two
+// neighbouring threads read one 32-byte sector); the 16 partial sums of each dim meet through
+// shuffles inside the half-warp. All rows (<= 8) reuse the loaded weights.
+constexpr int kAbsorbMaxRows = 8;
+__global__ void __launch_bounds__(256) mla_absorb_q_kernel(MlaAbsorbArgs a, int rows) {
+  __shared__ float qn[kAbsorbMaxRows][256];
   pdl_wait();
-  const int h = blockIdx.x, r = blockIdx.y, tid = threadIdx.x;
-  const float* q = a.q + ((int64_t)r * a.nh + h) * (a.nope + kMlaRope);
-  if (tid < a.nope) qn[tid] = q[tid];
-  __syncthreads();
-  const __nv_bfloat16* w = a.w_uk + (int64_t)h * a.nope * kMlaLat;
-  float acc0 = 0.f, acc1 = 0.f;
-  for (int i = 0; i < a.nope; ++i) {
-    acc0 += qn[i] * __bfloat162float(w[(int64_t)i * kMlaLat + tid]);
-    acc1 += qn[i] * __bfloat162float(w[(int64_t)i * kMlaLat + tid + 256]);
+  const int h = blockIdx.x, quarter = blockIdx.y, tid = threadIdx.x;
+  const int stride_q = a.nh * (a.nope + kMlaRope);
+  for (int i = tid; i < rows * a.nope; i += blockDim.x) {
+    const int r = i / a.nope, k = i % a.nope;
+    qn[r][k] = a.q[(int64_t)r * stride_q + (int64_t)h * (a.nope + kMlaRope) + k];
   }
-  float* ql = a.q_lat + ((int64_t)r * a.nh + h) * kMlaLat;
-  ql[tid] = acc0;
-  ql[tid + 256] = acc1;
-  if (tid < kMlaRope / 2) {
-    const int pos = a.positions[r];
-    float x = q[a.nope + tid], y = q[a.nope + tid + kMlaRope / 2];
-    const float* cs = a.rope + (int64_t)pos * kMlaRope + 2 * tid;
-    rope_neox_pair(x, y, cs[0], cs[1]);
-    float* qp = a.q_pe + ((int64_t)r * a.nh + h) * kMlaRope;
-    qp[tid] = x;
-    qp[tid + kMlaRope / 2] = y;
+  __syncthreads();
+  const int c8 = tid >> 4, ig = tid & 15;
+  const int d0 = quarter * 128 + c8 * 8;
+  const int per = a.nope / 16;
+  const __nv_bfloat16* w = a.w_uk + (int64_t)h * a.nope * kMlaLat + d0;
+  float acc[kAbsorbMaxRows][8];
+#pragma unroll
+  for (int r = 0; r < kAbsorbMaxRows; ++r)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[r][e] = 0.f;
+#pragma unroll 4
+  for (int ii = 0; ii < per; ++ii) {
+    const int i = ii * 16 + ig;
+    const uint4 u = *reinterpret_cast<const uint4*>(w + (int64_t)i * kMlaLat);
+    const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&u);
+    float wv[8];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(b2[e]);
+      wv[2 * e] = f.x;
+      wv[2 * e + 1] = f.y;
+    }
+#pragma unroll
+    for (int r = 0; r < kAbsorbMaxRows; ++r) {
+      if (r < rows) {
+        const float qv = qn[r][i];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[r][e] += qv * wv[e];
+      }
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < kAbsorbMaxRows; ++r) {
+    if (r < rows) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        float v = acc[r][e];
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        acc[r][e] = v;
+      }
+      if (ig == 0) {
+        float* dst = a.q_lat + ((int64_t)r * a.nh + h) * kMlaLat + d0;
+        *reinterpret_cast<float4*>(dst) = make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+        *reinterpret_cast<float4*>(dst + 4) = make_float4(acc[r][4], acc[r][5], acc[r][6], acc[r][7]);
+      }
+    }
+  }
+  if (quarter == 0) {
+    for (int o = tid; o < rows * (kMlaRope / 2); o += blockDim.x) {
+      const int r = o / (kMlaRope / 2), t = o % (kMlaRope / 2);
+      const float* q = a.q + (int64_t)r * stride_q + (int64_t)h * (a.nope + kMlaRope);
+      const int pos = a.positions[r];
+      float x = q[a.nope + t], y = q[a.nope + t + kMlaRope / 2];
+      const float* cs = a.rope + (int64_t)pos * kMlaRope + 2 * t;
+      rope_neox_pair(x, y, cs[0], cs[1]);
+      float* qp = a.q_pe + ((int64_t)r * a.nh + h) * kMlaRope;
+      qp[t] = x;
+      qp[t + kMlaRope / 2] = y;
+    }
   }
   pdl_launch();
 }
 
 void mla_absorb_q_launch(const MlaAbsorbArgs& a, int rows, cudaStream_t s, bool pdl) {
-  if (a.nope > 256) throw std::runtime_error("mla: nope dim must be <= 256");
-  launch(mla_absorb_q_kernel, dim3(a.nh, rows), dim3(256), 0, s, pdl, a);
+  if (a.nope > 256 || a.nope % 16) throw std::runtime_error("mla: nope dim must be a multiple of 16, <= 256");
+  if (rows > kAbsorbMaxRows) throw std::runtime_error("mla absorb: at most 8 rows");
+  launch(mla_absorb_q_kernel, dim3(a.nh, 4), dim3(256), 0, s, pdl, a, rows);
 }
 
 // ---- output: o[h] = W_UV[h] o_lat[h] -> q8 ------------------------------------------------------
-// Grid (heads, rows), 128 threads (4 warps); W_UV is [heads, v_dim, 512] bf16; warp-per-row.
-__global__ void __launch_bounds__(128) mla_out_kernel(MlaOutArgs a) {
-  __shared__ float ol[kMlaLat];
-  __shared__ float ov[256];
+// Grid (heads, vdim / 32): one CTA per 32 output dims of a head (one q8 block); 8 warps x 4
+// output rows, lanes over the 512 latent dims with 16-byte weight loads; all rows (<= 8) reuse
+// the loaded weights.
+constexpr int kOutMaxRows = 8;
+__global__ void __launch_bounds__(256) mla_out_kernel(MlaOutArgs a, int rows) {
+  __shared__ __align__(16) float ol[kOutMaxRows][kMlaLat];
+  __shared__ float ov[kOutMaxRows][32];
   pdl_wait();
-  const int h = blockIdx.x, r = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const float* src = a.o_lat + ((int64_t)r * a.nh + h) * kMlaLat;
-  for (int i = tid; i < kMlaLat; i += blockDim.x) ol[i] = src[i];
+  const int h = blockIdx.x, jb = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  for (int i = tid; i < rows * kMlaLat; i += blockDim.x) {
+    const int r = i / kMlaLat, d = i % kMlaLat;
+    ol[r][d] = a.o_lat[((int64_t)r * a.nh + h) * kMlaLat + d];
+  }
   __syncthreads();
-  const __nv_bfloat16* w = a.w_uv + (int64_t)h * a.vdim * kMlaLat;
-  for (int j = warp; j < a.vdim; j += 4) {
+  const __nv_bfloat16* w = a.w_uv + ((int64_t)h * a.vdim + jb * 32) * kMlaLat;
+#pragma unroll
+  for (int jj = 0; jj < 4; ++jj) {
+    const int j = warp * 4 + jj;
     const __nv_bfloat16* wr = w + (int64_t)j * kMlaLat;
-    float acc = 0.f;
-#pragma unroll 4
-    for (int k = lane; k < kMlaLat; k += 32) acc += __bfloat162float(wr[k]) * ol[k];
-    acc = warp_sum(acc);
-    if (lane == 0) ov[j] = acc;
+    float acc[kOutMaxRows];
+#pragma unroll
+    for (int r = 0; r < kOutMaxRows; ++r) acc[r] = 0.f;
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {  // 2 x 8 dims per lane covers 512
+      const int d0 = (c * 32 + lane) * 8;
+      const uint4 u = *reinterpret_cast<const uint4*>(wr + d0);
+      const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(b2[e]);
+#pragma unroll
+        for (int r = 0; r < kOutMaxRows; ++r)
+          if (r < rows) acc[r] += f.x * ol[r][d0 + 2 * e] + f.y * ol[r][d0 + 2 * e + 1];
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < kOutMaxRows; ++r) {
+      if (r < rows) {
+        const float v = warp_sum(acc[r]);
+        if (lane == 0) ov[r][j] = v;
+      }
+    }
   }
   __syncthreads();
   pdl_launch();
   const int64_t width = (int64_t)a.nh * a.vdim;
-  for (int j = tid; j < a.vdim; j += blockDim.x) {  // whole warps: vdim % 32 == 0
-    const float v = ov[j];
-    const int64_t col = (int64_t)h * a.vdim + j;
+  if (warp < rows) {  // warp r quantises row r's 32-dim block
+    const int r = warp;
+    const float v = ov[r][lane];
+    const int64_t col = (int64_t)h * a.vdim + jb * 32 + lane;
     const float amax = warp_max(fabsf(v));
     const float d = amax / 127.f;
     const int q = amax > 0.f ? __float2int_rn(v / d) : 0;
@@ -142,7 +219,8 @@ __global__ void __launch_bounds__(128) mla_out_kernel(MlaOutArgs a) {
 
 void mla_out_launch(const MlaOutArgs& a, int rows, cudaStream_t s, bool pdl) {
   if (a.vdim % 32 || a.vdim > 256) throw std::runtime_error("mla: v dim must be a multiple of 32, <= 256");
-  launch(mla_out_kernel, dim3(a.nh, rows), dim3(128), 0, s, pdl, a);
+  if (rows > kOutMaxRows) throw std::runtime_error("mla out: at most 8 rows");
+  launch(mla_out_kernel, dim3(a.nh, a.vdim / 32), dim3(256), 0, s, pdl, a, rows);
 }
 
 // ---- attention over the latent cache --------------------------------------------------------

@@ -75,32 +75,43 @@ __device__ __forceinline__ void block_argmax(float& v, int& i, float* sv, int* s
   }
 }
 
-// One CTA (256 threads) per token; E <= 1024.
-__global__ void __launch_bounds__(256) moe_topk_kernel(MoeTopkArgs a) {
-  __shared__ float score[1024], sel[1024];
-  __shared__ float sv[32];
-  __shared__ int si[32];
-  __shared__ float gscore[64];
-  __shared__ int keep_group[64];
-  __shared__ float red[32];
-  pdl_wait();
-  const int t = blockIdx.x, E = a.E, tid = threadIdx.x;
+// Top-k of token t by one CTA of 256 threads; E <= 1024. Logits are read with .cg loads (the
+// fused router writes them from other CTAs of the same launch).
+struct TopkSmem {
+  float score[1024], sel[1024];
+  float sv[32];
+  int si[32];
+  float gscore[64];
+  int keep_group[64];
+  float red[32];
+  int ids[32];
+  float ws[32];
+};
+__device__ void topk_token(const MoeTopkArgs& a, int t, TopkSmem& sm) {
+  float* score = sm.score;
+  float* sel = sm.sel;
+  float* sv = sm.sv;
+  int* si = sm.si;
+  float* gscore = sm.gscore;
+  int* keep_group = sm.keep_group;
+  float* red = sm.red;
+  const int E = a.E, tid = threadIdx.x;
   const float* l = a.logits + (int64_t)t * E;
   // scores
   if (a.scoring == 0) {  // softmax
     float m = -INFINITY;
-    for (int e = tid; e < E; e += blockDim.x) m = fmaxf(m, l[e]);
+    for (int e = tid; e < E; e += blockDim.x) m = fmaxf(m, __ldcg(l + e));
     m = block_max(m, red);
     float z = 0.f;
-    for (int e = tid; e < E; e += blockDim.x) z += __expf(l[e] - m);
+    for (int e = tid; e < E; e += blockDim.x) z += __expf(__ldcg(l + e) - m);
     z = block_sum(z, red);
     for (int e = tid; e < E; e += blockDim.x) {
-      score[e] = __expf(l[e] - m) / z;
+      score[e] = __expf(__ldcg(l + e) - m) / z;
       sel[e] = score[e];
     }
   } else {  // sigmoid; selection adds the learned bias
     for (int e = tid; e < E; e += blockDim.x) {
-      score[e] = 1.f / (1.f + __expf(-l[e]));
+      score[e] = 1.f / (1.f + __expf(-__ldcg(l + e)));
       sel[e] = score[e] + (a.bias ? a.bias[e] : 0.f);
     }
   }
@@ -133,8 +144,8 @@ __global__ void __launch_bounds__(256) moe_topk_kernel(MoeTopkArgs a) {
     __syncthreads();
   }
   float wsum = 0.f;
-  __shared__ int ids[32];
-  __shared__ float ws[32];
+  int* ids = sm.ids;
+  float* ws = sm.ws;
   for (int k = 0; k < a.k; ++k) {
     float v = -INFINITY;
     int i = 0x7fffffff;
@@ -159,6 +170,13 @@ __global__ void __launch_bounds__(256) moe_topk_kernel(MoeTopkArgs a) {
     a.weights[(int64_t)t * a.k + tid] = w * a.scale;
   }
   (void)wsum;
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(256) moe_topk_kernel(MoeTopkArgs a) {
+  __shared__ TopkSmem sm;
+  pdl_wait();
+  topk_token(a, blockIdx.x, sm);
   pdl_launch();
 }
 
@@ -166,6 +184,111 @@ void moe_topk_launch(const MoeTopkArgs& a, cudaStream_t s, bool pdl) {
   if (a.E > 1024 || a.k > 32) throw std::runtime_error("moe_topk: E <= 1024 and k <= 32");
   if (a.n_groups > 64 || (a.n_groups > 1 && a.E % a.n_groups)) throw std::runtime_error("moe_topk: bad groups");
   launch(moe_topk_kernel, dim3(a.T), dim3(256), 0, s, pdl, a);
+}
+
+// ---- fused routing (decode): router GEMV + top-k + counting sort + active list, one launch --------
+// Every CTA computes router logits for its experts (4 warps per expert, each a quarter of K,
+// joined in shared memory). The CTA whose arrival completes the grid (device-scope counter, reset
+// by it afterwards) then runs top-k for every token, the counting sort of the (token, slot) pairs
+// by expert (plus one shared-expert pair per token as expert E), and the compact list of experts
+// with pairs. No activation gather: the expert kernels read each pair's token row directly.
+constexpr int kRouteExpertsPerCta = 2;
+__global__ void __launch_bounds__(256) moe_route_kernel(MoeRouteArgs a) {
+  __shared__ TopkSmem sm;
+  __shared__ float part[kRouteExpertsPerCta][8][4];
+  __shared__ int cnt[1025], off[1026];
+  __shared__ bool last;
+  pdl_wait();
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int T = a.T, E = a.E, K = a.K;
+  {  // logits of experts e0 .. e0 + 1 for every token: warp = (expert slot, quarter)
+    const int es = warp >> 2, qt = warp & 3;
+    const int e = blockIdx.x * kRouteExpertsPerCta + es;
+    const int kq = K / 4;
+    if (e < E) {
+      const float* wr = a.router + (int64_t)e * K + qt * kq;
+      for (int t = 0; t < T; ++t) {
+        const int8_t* xq = a.xq + (int64_t)t * a.x_stride_q + qt * kq;
+        const float* xd = a.xd + (int64_t)t * a.x_stride_s + (qt * kq >> 5);
+        float acc = 0.f;
+        for (int k = lane * 4; k < kq; k += 128) {
+          const float4 wv = *reinterpret_cast<const float4*>(wr + k);
+          const char4 qv = *reinterpret_cast<const char4*>(xq + k);
+          acc += (wv.x * qv.x + wv.y * qv.y + wv.z * qv.z + wv.w * qv.w) * xd[k >> 5];
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) part[es][t][qt] = acc;
+      }
+    }
+    __syncthreads();
+    if (tid < kRouteExpertsPerCta * T) {
+      const int es2 = tid / T, t = tid % T;
+      const int e2 = blockIdx.x * kRouteExpertsPerCta + es2;
+      if (e2 < E) a.logits[(int64_t)t * E + e2] = part[es2][t][0] + part[es2][t][1] + part[es2][t][2] + part[es2][t][3];
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) last = atomicAdd(a.counter, 1) == (int)gridDim.x - 1;
+  __syncthreads();
+  if (!last) {
+    pdl_launch();
+    return;
+  }
+  __threadfence();
+  MoeTopkArgs ta{};
+  ta.logits = a.logits;
+  ta.bias = a.bias;
+  ta.T = T;
+  ta.E = E;
+  ta.k = a.k;
+  ta.scoring = a.scoring;
+  ta.n_groups = a.n_groups;
+  ta.topk_groups = a.topk_groups;
+  ta.renorm = a.renorm;
+  ta.scale = a.scale;
+  ta.ids = a.ids;
+  ta.weights = a.weights;
+  for (int t = 0; t < T; ++t) topk_token(ta, t, sm);
+  // counting sort of the pairs by expert (ids written above by this CTA)
+  const int P = T * a.k, E1 = E + (a.shared ? 1 : 0);
+  for (int e = tid; e < E1; e += blockDim.x) cnt[e] = 0;
+  __syncthreads();
+  for (int p = tid; p < P; p += blockDim.x) atomicAdd(&cnt[a.ids[p]], 1);
+  if (a.shared && tid == 0) cnt[E] = T;
+  __syncthreads();
+  if (tid == 0) {
+    off[0] = 0;
+    int n = 0;
+    for (int e = 0; e < E1; ++e) {
+      off[e + 1] = off[e] + cnt[e];
+      if (cnt[e] > 0) a.active[n++] = e;
+    }
+    *a.n_active = n;
+    *a.counter = 0;  // ready for the next launch
+  }
+  __syncthreads();
+  for (int e = tid; e < E1; e += blockDim.x) {
+    a.counts[e] = cnt[e];
+    a.offsets[e] = off[e];
+  }
+  if (tid < E) {
+    int pos = off[tid];
+    for (int p = 0; p < P; ++p)
+      if (a.ids[p] == tid) a.sorted[pos++] = p;
+  }
+  if (a.shared)
+    for (int t = tid; t < T; t += blockDim.x) a.sorted[P + t] = P + t;
+  pdl_launch();
+}
+
+void moe_route_launch(const MoeRouteArgs& a, cudaStream_t s, bool pdl) {
+  if (a.E + (a.shared ? 1 : 0) > 1024 || a.k > 32) throw std::runtime_error("moe_route: E <= 1023 and k <= 32");
+  if (a.T > 8) throw std::runtime_error("moe_route: at most 8 tokens (decode)");
+  if (a.K % 512) throw std::runtime_error("moe_route: hidden must be a multiple of 512");
+  if (a.n_groups > 64 || (a.n_groups > 1 && a.E % a.n_groups)) throw std::runtime_error("moe_route: bad groups");
+  const int ctas = (a.E + kRouteExpertsPerCta - 1) / kRouteExpertsPerCta;
+  launch(moe_route_kernel, dim3(ctas), dim3(256), 0, s, pdl, a);
 }
 
 // ---- align (counting sort by expert) + gather ---------------------------------------------------

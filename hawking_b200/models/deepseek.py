@@ -162,6 +162,8 @@ class DeepSeekModel:
         self.sorted = torch.zeros(R * k + R, dtype=torch.int32, device=dev)
         self.active = torch.zeros(E + 1, dtype=torch.int32, device=dev)
         self.n_active = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.route_counter = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.fused_route = cfg.hidden % 512 == 0 and E + 1 <= 1024
         self.gx = Q8Act(R * k + R, H, dev)
         self.hx = Q8Act(R * k + R, F, dev)
         self.hs = Q8Act(R, Fs, dev)
@@ -205,19 +207,28 @@ class DeepSeekModel:
             mixed_gemv(t, L.idx["d"], h, self.x[:rows], residual=True)
             return
         E, k, H, F = cfg.n_experts, cfg.top_k, cfg.hidden, cfg.expert_ffn
-        ops.router_logits(L.router, xa, self.rlog[:rows])
-        ops.moe_topk(self.rlog[:rows], L.router_bias, k, 1, cfg.n_groups, cfg.topk_groups, cfg.norm_topk,
-                     cfg.routed_scale, self.ids[:rows], self.rw[:rows])
         fold = self.fold_shared and L.idx["sg"] == L.idx["eg"] + E and L.idx["su"] == L.idx["eu"] + E and \
             L.idx["sd"] == L.idx["ed"] + E
-        ops.moe_align(self.ids[:rows], E, xa, self.counts, self.offsets, self.sorted, self.gx, shared=fold)
         K = kernels()
-        ops.launches.add(3)
-        K.moe_active(self.counts, self.active, self.n_active, ops.PDL)
+        if self.fused_route:
+            # one launch: router GEMV, top-k, sort by expert, active list; experts read token rows
+            ops.moe_route(L.router, xa, k, 1, L.router_bias, cfg.n_groups, cfg.topk_groups, cfg.norm_topk,
+                          cfg.routed_scale, self.rlog[:rows], self.ids[:rows], self.rw[:rows], self.counts,
+                          self.offsets, self.sorted, self.active, self.n_active, fold, self.route_counter)
+            gin = xa
+        else:
+            ops.router_logits(L.router, xa, self.rlog[:rows])
+            ops.moe_topk(self.rlog[:rows], L.router_bias, k, 1, cfg.n_groups, cfg.topk_groups, cfg.norm_topk,
+                         cfg.routed_scale, self.ids[:rows], self.rw[:rows])
+            ops.moe_align(self.ids[:rows], E, xa, self.counts, self.offsets, self.sorted, self.gx, shared=fold)
+            ops.launches.add()
+            K.moe_active(self.counts, self.active, self.n_active, ops.PDL)
+            gin = self.gx
+        ops.launches.add(2)
         na = min(E, rows * k) + (1 if fold else 0)
         K.moe_mixed_gemv(0, t.descs, L.idx["eg"], L.idx["eu"], F, H, k, self.counts, self.offsets, self.sorted,
-                         self.active, self.n_active, na, self.gx.q, self.gx.d, self.gx.s, self.hx.q, self.hx.d,
-                         self.hx.s, None, None, ops.PDL)
+                         self.active, self.n_active, na, gin.q, gin.d, gin.s, self.hx.q, self.hx.d,
+                         self.hx.s, None, None, ops.PDL, rows * k, self.fused_route)
         K.moe_mixed_gemv(1, t.descs, L.idx["ed"], L.idx["ed"], H, F, k, self.counts, self.offsets, self.sorted,
                          self.active, self.n_active, na, self.hx.q, self.hx.d, self.hx.s, None, None, None,
                          self.x[:rows], self.rw[:rows].reshape(-1), ops.PDL, rows * k)

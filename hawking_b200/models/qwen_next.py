@@ -184,6 +184,8 @@ class QwenNextModel:
         self.sorted = torch.zeros(R * k, dtype=torch.int32, device=dev)
         self.active = torch.zeros(E, dtype=torch.int32, device=dev)
         self.n_active = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.route_counter = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.fused_route = cfg.hidden % 512 == 0 and E < 1024
         self.gx = Q8Act(R * k, H, dev)
         self.hx = Q8Act(R * k, F, dev)
         self.hs = Q8Act(R, Fs, dev)
@@ -248,17 +250,25 @@ class QwenNextModel:
         cfg, t = self.cfg, self.w.table
         E, k, H, F = cfg.n_experts, cfg.top_k, cfg.hidden, cfg.expert_ffn
         xa = self.xa.view(rows)
-        ops.router_logits(L.router, xa, self.rlog[:rows])
         ops.router_logits(L.shared_gate, xa, self.sglog[:rows])
-        ops.moe_topk(self.rlog[:rows], None, k, 0, 1, 1, cfg.norm_topk, 1.0, self.ids[:rows], self.rw[:rows])
-        ops.moe_align(self.ids[:rows], E, xa, self.counts, self.offsets, self.sorted, self.gx)
         K = kernels()
-        ops.launches.add(3)
-        K.moe_active(self.counts, self.active, self.n_active, ops.PDL)
+        if self.fused_route:  # router GEMV, top-k, sort by expert and active list in one launch
+            ops.moe_route(L.router, xa, k, 0, None, 1, 1, cfg.norm_topk, 1.0, self.rlog[:rows], self.ids[:rows],
+                          self.rw[:rows], self.counts, self.offsets, self.sorted, self.active, self.n_active, False,
+                          self.route_counter)
+            gin = xa
+        else:
+            ops.router_logits(L.router, xa, self.rlog[:rows])
+            ops.moe_topk(self.rlog[:rows], None, k, 0, 1, 1, cfg.norm_topk, 1.0, self.ids[:rows], self.rw[:rows])
+            ops.moe_align(self.ids[:rows], E, xa, self.counts, self.offsets, self.sorted, self.gx)
+            ops.launches.add()
+            K.moe_active(self.counts, self.active, self.n_active, ops.PDL)
+            gin = self.gx
+        ops.launches.add(2)
         na = min(E, rows * k)
         K.moe_mixed_gemv(0, t.descs, L.idx["eg"], L.idx["eu"], F, H, k, self.counts, self.offsets, self.sorted,
-                         self.active, self.n_active, na, self.gx.q, self.gx.d, self.gx.s, self.hx.q, self.hx.d,
-                         self.hx.s, None, None, ops.PDL)
+                         self.active, self.n_active, na, gin.q, gin.d, gin.s, self.hx.q, self.hx.d,
+                         self.hx.s, None, None, ops.PDL, rows * k, self.fused_route)
         K.moe_mixed_gemv(1, t.descs, L.idx["ed"], L.idx["ed"], H, F, k, self.counts, self.offsets, self.sorted,
                          self.active, self.n_active, na, self.hx.q, self.hx.d, self.hx.s, None, None, None,
                          self.x[:rows], self.rw[:rows].reshape(-1), ops.PDL)

@@ -229,6 +229,16 @@ def moe_topk(logits, bias, k: int, scoring: int, n_groups: int, topk_groups: int
     kernels().moe_topk(logits, bias, k, scoring, n_groups, topk_groups, renorm, scale, ids, weights, PDL)
 
 
+def moe_route(router, x: Q8Act, k: int, scoring: int, bias, n_groups: int, topk_groups: int, renorm: bool,
+              scale: float, logits, ids, weights, counts, offsets, sorted_pairs, active, n_active, shared: bool,
+              counter):
+    """Fused decode routing (one launch): router logits, top-k, the pairs sorted by expert (plus
+    the shared expert as expert E when ``shared``) and the list of experts with pairs."""
+    launches.add()
+    kernels().moe_route(router, x.q, x.d, k, scoring, bias, n_groups, topk_groups, renorm, scale, logits, ids,
+                        weights, counts, offsets, sorted_pairs, active, n_active, shared, counter, PDL)
+
+
 def moe_align(ids, E: int, x: Q8Act, counts, offsets, sorted_pairs, gathered: Q8Act, shared: bool = False):
     """Counting sort of the (token, expert) pairs by expert plus the gather of their q8 rows;
     ``shared`` appends expert E (a shared expert) with one pair per token after the routed ones."""
