@@ -171,25 +171,42 @@ def profile_one_step(m, kv, ctx):
 
 
 def bench_deepseek(args):
-    """DeepSeek-V3-style MLA + MoE (config 5): bs1 / bs8 device-timed decode on one GPU with
-    random-init fp8 e4m3 (128 x 128 block-scaled) weights of the full 43-layer architecture."""
+    """DeepSeek-V3-style MLA + MoE (config 5): bs1 / bs8 device-timed decode with random-init fp8
+    e4m3 (128 x 128 block-scaled) weights of the full 43-layer architecture; on N > 1 ranks the
+    model is tensor parallel over heads and expert parallel over the 256 experts (parallel/ep.py)."""
     import torch
+    import torch.distributed as dist
     from hawking_b200.models.config import preset
     from hawking_b200.models.deepseek import DeepSeekModel, LatentCache, random_deepseek_weights
     from hawking_b200.utils.clocks import ClockSampler
-    dev = torch.device("cuda", 0)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
     K, W, ctx = args.steps, args.warmup, args.ctx
     cfg = preset("deepseek-v3", max_ctx=ctx + 2 * (K + W) + 64)
     if args.layers:
         cfg = cfg.with_(layers=args.layers)
     t0 = time.time()
-    w = random_deepseek_weights(cfg, dev, seed=0)
+    tp = None
+    if world > 1:
+        from hawking_b200.parallel.ep import local_deepseek_config, random_deepseek_weights_ep
+        from hawking_b200.parallel.tp import TPComm
+        w = random_deepseek_weights_ep(cfg, rank, world, dev, seed=0)
+        tp = TPComm(rank, world, 2 * cfg.layers, 8, cfg.hidden, dev)
+        mcfg = local_deepseek_config(cfg, world)
+    else:
+        w = random_deepseek_weights(cfg, dev, seed=0)
+        mcfg = cfg
     t_load = time.time() - t0
     bs, max_seqs = 64, 8
     max_blocks = -(-cfg.max_ctx // bs)
     kv = LatentCache(cfg.layers, max_seqs * max_blocks + 8, bs, max_seqs, max_blocks, dev)
-    m = DeepSeekModel(cfg, w, kv, max_rows=8, device=dev)
+    m = DeepSeekModel(mcfg, w, kv, max_rows=8, device=dev, tp=tp)
     g = torch.Generator(device=dev).manual_seed(1)
     for lat in kv.latent:
         lat.normal_(0, 1, generator=g)
@@ -204,20 +221,34 @@ def bench_deepseek(args):
             pos.append(ctx)
             rseq.append(kv.row(sid))
             rctx.append(ctx + 1)
+        if world > 1:  # every rank decodes the same token ids (the hidden state is replicated)
+            t = torch.tensor(ids, dtype=torch.int32, device=dev)
+            dist.broadcast(t, 0)
+            ids = t.tolist()
         m.inp.upload(ids, pos, [0] * nseq, rseq, rctx)
         for _ in range(W):
             m.graph_forward(nseq, "greedy", advance=True)
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with ClockSampler(0, period_ms=50) as cs:
+        with ClockSampler(local, period_ms=50) as cs:
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize()
             e0.record()
             for _ in range(K):
                 m.graph_forward(nseq, "greedy", advance=True)
             e1.record()
             torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
         for i in range(nseq):
             kv.drop(10 + i)
-        return e0.elapsed_time(e1) / K, cs.result
+        ms = e0.elapsed_time(e1) / K
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = t.item()
+        return ms, cs.result
 
     if args.profile_step:
         profile_one_step(m, kv, ctx)
@@ -225,9 +256,13 @@ def bench_deepseek(args):
     ms1, clocks = timed(1)
     launches = m.launches_per_graph
     ms8, clocks8 = timed(8)
+    if tp is not None:
+        tp.check()
+        m.release_graphs() if hasattr(m, "release_graphs") else m._graphs.clear()
+        tp.close()
     out = {
-        "metric": "decode tok/s bs1 (DeepSeek-V3-style MLA + MoE, fp8 e4m3 block-scaled), 1 GPU",
-        "value": round(1000.0 / ms1, 2), "unit": "tok/s", "n_gpus": 1, "steps": K, "warmup": W,
+        "metric": "decode tok/s bs1 (DeepSeek-V3-style MLA + MoE, fp8 e4m3 block-scaled), %d GPU" % world,
+        "value": round(1000.0 / ms1, 2), "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": round(ms1, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "fp8 e4m3 weights with 128x128 fp32 block scales x int8 activation blocks, fp32 accumulate, "
                  "bf16 latent cache, bf16 W_UK/W_UV",
@@ -236,14 +271,19 @@ def bench_deepseek(args):
         "config": {"model": "deepseek-v3-style (%d layers, hidden 4096, 64 heads, q_lora 1024, kv_lora 512, rope 64, "
                             "nope 128, v 128, 256 experts top-8 sigmoid+bias group-limited, 1 shared, expert FFN 1024, "
                             "3 dense layers FFN 11264, vocab 129280)" % cfg.layers,
-                   "global_batch": 1, "seq_len": ctx, "parallelism": "tp1",
-                   "l2": "inputs larger than L2: %.1f GB of weights resident" % (w.nbytes / 1e9)},
+                   "global_batch": 1, "seq_len": ctx,
+                   "parallelism": "tp1" if world == 1 else "tp%d attention + ep%d experts" % (world, world),
+                   "l2": "inputs larger than L2: %.1f GB of weights resident per GPU" % (w.nbytes / 1e9)},
         "clocks": clocks, "e2e": None, "e2e_note": "no engine/scheduler integration for the MLA model yet",
         "gpu_launches": launches * K,
         "bs8": {"tok_s_aggregate": round(8 * 1000.0 / ms8, 1), "ms_per_step": round(ms8, 4), "clocks": clocks8},
         "weights_gb": round(w.nbytes / 1e9, 2), "load_s": round(t_load, 1),
     }
-    print(json.dumps(out))
+    if rank == 0:
+        print(json.dumps(out))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
     return 0
 
 

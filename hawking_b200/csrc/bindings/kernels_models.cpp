@@ -67,8 +67,22 @@ Tensor mixed_descs(const std::vector<Tensor>& codes, const std::vector<Tensor>& 
 
 void mixed_gemv(int64_t epi, const Tensor& descs, int64_t d0, int64_t d1, int64_t N, int64_t K, const Tensor& xq,
                 const Tensor& xd, const Tensor& xs, const optional<Tensor>& y, double alpha, const optional<Tensor>& oq,
-                const optional<Tensor>& od, const optional<Tensor>& os, bool pdl, const optional<Tensor>& gate_logit) {
+                const optional<Tensor>& od, const optional<Tensor>& os, bool pdl, const optional<Tensor>& gate_logit,
+                const optional<Tensor>& push_table, const optional<Tensor>& push_epoch,
+                const optional<Tensor>& argmax_slots, int64_t argmax_offset) {
   hk::MixedGemvArgs a{};
+  if (argmax_slots.has_value()) {
+    TORCH_CHECK(argmax_slots->scalar_type() == at::kLong && argmax_slots->size(0) >= xq.size(0) &&
+                    argmax_slots->size(1) == hk::kArgmaxSlots, "mixed_gemv: argmax slots [rows, 256] int64");
+    a.argmax_slots = reinterpret_cast<unsigned long long*>(argmax_slots->data_ptr<int64_t>());
+    a.argmax_offset = argmax_offset;
+  }
+  if (push_table.has_value()) {
+    TORCH_CHECK(push_table->scalar_type() == at::kLong && push_epoch.has_value(), "mixed_gemv push: int64 table + epoch");
+    a.push_recv = reinterpret_cast<unsigned long long* const*>(push_table->data_ptr<int64_t>());
+    a.push_n = (int)push_table->numel();
+    a.push_epoch = push_epoch->data_ptr<int>();
+  }
   a.desc = reinterpret_cast<const hk::MixedDesc*>(descs.data_ptr());
   a.d0 = (int)d0;
   a.d1 = (int)d1;
@@ -96,7 +110,8 @@ void mixed_gemv(int64_t epi, const Tensor& descs, int64_t d0, int64_t d1, int64_
     a.o_stride_q = oq->stride(0);
     a.o_stride_s = od->stride(0);
   }
-  TORCH_CHECK(epi == hk::EPI_SWIGLU_Q8 ? a.oq != nullptr : a.y != nullptr, "mixed_gemv: output missing");
+  TORCH_CHECK(epi == hk::EPI_SWIGLU_Q8 ? a.oq != nullptr : (epi == hk::EPI_PUSH ? a.push_recv != nullptr : a.y != nullptr),
+              "mixed_gemv: output missing");
   const c10::cuda::CUDAGuard g(xq.device());
   hk::mixed_gemv_launch((int)epi, a, cur_stream(), pdl);
 }
@@ -111,8 +126,18 @@ void moe_mixed_gemv(int64_t epi, const Tensor& descs, int64_t base0, int64_t bas
                     const Tensor& n_active, int64_t max_active, const Tensor& xq, const Tensor& xd, const Tensor& xs,
                     const optional<Tensor>& oq, const optional<Tensor>& od, const optional<Tensor>& os,
                     const optional<Tensor>& y, const optional<Tensor>& route_w, bool pdl, int64_t routed_pairs,
-                    bool direct) {
+                    bool direct, int64_t e_lo, int64_t e_count, int64_t T, const optional<Tensor>& push_table,
+                    const optional<Tensor>& push_epoch) {
   hk::MoeMixedArgs a{};
+  a.e_lo = (int)e_lo;
+  a.e_count = (int)e_count;
+  a.T = (int)T;
+  if (push_table.has_value()) {
+    TORCH_CHECK(push_table->scalar_type() == at::kLong && push_epoch.has_value(), "moe_mixed_gemv push: int64 table + epoch");
+    a.push_recv = reinterpret_cast<unsigned long long* const*>(push_table->data_ptr<int64_t>());
+    a.push_n = (int)push_table->numel();
+    a.push_epoch = push_epoch->data_ptr<int>();
+  }
   a.routed_pairs = routed_pairs < 0 ? INT_MAX : (int)routed_pairs;
   a.direct = direct ? 1 : 0;
   a.x_stride_q = xq.stride(0);
@@ -140,7 +165,9 @@ void moe_mixed_gemv(int64_t epi, const Tensor& descs, int64_t base0, int64_t bas
     a.y_stride = y->stride(0);
   }
   a.route_w = optr<float>(route_w);
-  TORCH_CHECK(epi == 0 ? a.oq != nullptr : (a.y != nullptr && a.route_w != nullptr), "moe_mixed_gemv: outputs");
+  TORCH_CHECK(epi == 0 ? a.oq != nullptr : (epi == 2 ? (a.push_recv != nullptr && a.route_w != nullptr)
+                                                      : (a.y != nullptr && a.route_w != nullptr)),
+              "moe_mixed_gemv: outputs");
   const c10::cuda::CUDAGuard g(xq.device());
   hk::moe_mixed_gemv_launch((int)epi, a, (int)max_active, cur_stream(), pdl);
 }
@@ -364,7 +391,8 @@ void register_model_kernels(py::module_& m) {
   m.def("mixed_gemv", &mixed_gemv, py::arg("epi"), py::arg("descs"), py::arg("d0"), py::arg("d1"), py::arg("N"),
         py::arg("K"), py::arg("xq"), py::arg("xd"), py::arg("xs"), py::arg("y") = py::none(), py::arg("alpha") = 1.0,
         py::arg("oq") = py::none(), py::arg("od") = py::none(), py::arg("os") = py::none(), py::arg("pdl") = false,
-        py::arg("gate_logit") = py::none());
+        py::arg("gate_logit") = py::none(), py::arg("push_table") = py::none(), py::arg("push_epoch") = py::none(),
+        py::arg("argmax_slots") = py::none(), py::arg("argmax_offset") = 0);
   m.def("moe_active", &moe_active, py::arg("counts"), py::arg("active"), py::arg("n_active"), py::arg("pdl") = false);
   m.def("moe_mixed_gemv", &moe_mixed_gemv, py::arg("epi"), py::arg("descs"), py::arg("base0"), py::arg("base1"),
         py::arg("N"), py::arg("K"), py::arg("k"), py::arg("counts"), py::arg("offsets"), py::arg("sorted"),
@@ -372,7 +400,8 @@ void register_model_kernels(py::module_& m) {
         py::arg("oq") = py::none(), py::arg("od") = py::none(), py::arg("os") = py::none(), py::arg("y") = py::none(),
         py::arg("route_w") = py::none(), py::arg("pdl") = false,
         py::arg("routed_pairs") = -1,
-        py::arg("direct") = false);
+        py::arg("direct") = false, py::arg("e_lo") = 0, py::arg("e_count") = 0, py::arg("T") = 0,
+        py::arg("push_table") = py::none(), py::arg("push_epoch") = py::none());
   m.def("deltanet_conv", &deltanet_conv, py::arg("qkvz"), py::arg("conv_w"), py::arg("conv_state"), py::arg("slot"),
         py::arg("kh"), py::arg("r"), py::arg("dk"), py::arg("dv"), py::arg("kc"), py::arg("eps"), py::arg("q"),
         py::arg("k"), py::arg("v"), py::arg("z"), py::arg("pdl") = false);

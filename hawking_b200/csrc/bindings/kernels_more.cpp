@@ -105,9 +105,11 @@ void moe_route(const Tensor& router, const Tensor& xq, const Tensor& xd, int64_t
                const c10::optional<Tensor>& bias, int64_t n_groups, int64_t topk_groups, bool renorm, double scale,
                const Tensor& logits, const Tensor& ids, const Tensor& weights, const Tensor& counts,
                const Tensor& offsets, const Tensor& sorted, const Tensor& active, const Tensor& n_active, bool shared,
-               const Tensor& counter, bool pdl) {
+               const Tensor& counter, bool pdl, int64_t e_lo, int64_t e_hi) {
   TORCH_CHECK(router.scalar_type() == at::kFloat && router.dim() == 2, "moe_route: fp32 router [E, K]");
   hk::MoeRouteArgs a{};
+  a.e_lo = (int)e_lo;
+  a.e_hi = (int)e_hi;
   a.router = router.data_ptr<float>();
   a.E = (int)router.size(0);
   a.K = (int)router.size(1);
@@ -172,8 +174,17 @@ void moe_gemv(int64_t fmt, int64_t epi, const std::vector<Tensor>& w0, const std
               int64_t K, int64_t E, int64_t k, const Tensor& counts, const Tensor& offsets, const Tensor& sorted,
               const Tensor& xq, const Tensor& xd, const Tensor& xs, const c10::optional<Tensor>& oq,
               const c10::optional<Tensor>& od, const c10::optional<Tensor>& os, const c10::optional<Tensor>& y,
-              const c10::optional<Tensor>& route_w, bool pdl) {
+              const c10::optional<Tensor>& route_w, bool pdl, int64_t e_lo, int64_t T,
+              const c10::optional<Tensor>& push_table, const c10::optional<Tensor>& push_epoch) {
   hk::MoeGemvArgs a{};
+  a.e_lo = (int)e_lo;
+  a.T = (int)T;
+  if (push_table.has_value()) {
+    TORCH_CHECK(push_table->scalar_type() == at::kLong && push_epoch.has_value(), "moe_gemv push: int64 table + epoch");
+    a.push_recv = reinterpret_cast<unsigned long long* const*>(push_table->data_ptr<int64_t>());
+    a.push_n = (int)push_table->numel();
+    a.push_epoch = push_epoch->data_ptr<int>();
+  }
   a.w0 = planes_of(w0);
   if (!w1.empty()) a.w1 = planes_of(w1);
   a.N = (int)N;
@@ -191,6 +202,9 @@ void moe_gemv(int64_t fmt, int64_t epi, const std::vector<Tensor>& w0, const std
     a.oq = oq->data_ptr<int8_t>();
     a.od = od->data_ptr<float>();
     a.os = os->data_ptr<float>();
+  } else if (epi == 2) {
+    TORCH_CHECK(route_w.has_value() && a.push_recv, "moe_gemv combine push: route weights and push table required");
+    a.route_w = route_w->data_ptr<float>();
   } else {
     TORCH_CHECK(y.has_value() && route_w.has_value(), "moe_gemv down: y and route weights required");
     a.y = y->data_ptr<float>();
@@ -218,7 +232,7 @@ void register_more_kernels(py::module_& m) {
         py::arg("bias"), py::arg("n_groups"), py::arg("topk_groups"), py::arg("renorm"), py::arg("scale"),
         py::arg("logits"), py::arg("ids"), py::arg("weights"), py::arg("counts"), py::arg("offsets"),
         py::arg("sorted"), py::arg("active"), py::arg("n_active"), py::arg("shared"), py::arg("counter"),
-        py::arg("pdl") = false);
+        py::arg("pdl") = false, py::arg("e_lo") = 0, py::arg("e_hi") = 0);
   m.def("moe_align", &moe_align, py::arg("ids"), py::arg("E"), py::arg("xq"), py::arg("xd"), py::arg("xs"),
         py::arg("counts"), py::arg("offsets"), py::arg("sorted"), py::arg("gq"), py::arg("gd"), py::arg("gs"),
         py::arg("pdl") = false,
@@ -227,7 +241,8 @@ void register_more_kernels(py::module_& m) {
         py::arg("K"), py::arg("E"), py::arg("k"), py::arg("counts"), py::arg("offsets"), py::arg("sorted"),
         py::arg("xq"), py::arg("xd"), py::arg("xs"), py::arg("oq") = py::none(), py::arg("od") = py::none(),
         py::arg("os") = py::none(), py::arg("y") = py::none(), py::arg("route_w") = py::none(),
-        py::arg("pdl") = false);
+        py::arg("pdl") = false, py::arg("e_lo") = 0, py::arg("T") = 0, py::arg("push_table") = py::none(),
+        py::arg("push_epoch") = py::none());
   m.def("swiglu_bf16", &swiglu_bf16, py::arg("gu"), py::arg("F"), py::arg("h"), py::arg("clear") = true,
         py::arg("pdl") = false);
 }

@@ -252,6 +252,9 @@ struct MoeRouteArgs {           // fused decode routing (moe.cu)
   int* n_active;
   int shared;                   // append the shared expert as expert E
   int* counter;                 // zero-initialised arrival counter (reset by the kernel)
+  // expert parallelism: only experts in [e_lo, e_hi) (this rank's) enter the active list
+  // (e_hi == 0: every expert); counts, offsets and sorted still cover all E experts
+  int e_lo, e_hi;
 };
 void moe_route_launch(const MoeRouteArgs& a, cudaStream_t s, bool pdl);
 
@@ -287,6 +290,14 @@ struct MoeGemvArgs {
   float* y;              // epi 1: residual [T, y_stride] (atomic add of route_w * y)
   int64_t y_stride;
   const float* route_w;  // [T*k]
+  // expert parallelism: w0/w1 stack only experts [e_lo, e_lo + E) of the global numbering
+  int e_lo;
+  // epi 2 (expert-parallel combine): per token, the route-weighted sum over this rank's experts
+  // is pushed to every rank's receive region as flagged words (see EpPush)
+  int T;
+  unsigned long long* const* push_recv;
+  const int* push_epoch;
+  int push_n;
 };
 void moe_gemv_launch(int fmt, int epi, const MoeGemvArgs& a, cudaStream_t s, bool pdl);
 
@@ -317,6 +328,13 @@ struct MixedGemvArgs {
   float* od;
   float* os;
   int64_t o_stride_q, o_stride_s;
+  // EPI_PUSH: row-parallel projection pushed to every rank (same word layout as GemvArgs)
+  unsigned long long* const* push_recv;
+  const int* push_epoch;
+  int push_n;
+  // EPI_STORE greedy fusion (as GemvArgs): packed (value, row + argmax_offset) keys, atomicMax
+  unsigned long long* argmax_slots;
+  int64_t argmax_offset;
 };
 void mixed_gemv_launch(int epi, const MixedGemvArgs& a, cudaStream_t s, bool pdl);
 struct MoeMixedArgs {
@@ -341,6 +359,14 @@ struct MoeMixedArgs {
                               // the rest are shared-expert pairs (token pair - routed_pairs, weight 1)
   int direct;                 // epi 0: read each pair's token row of xq/xd/xs (strides below)
   int64_t x_stride_q, x_stride_s;
+  // expert parallelism: the table holds this rank's experts e_lo .. e_lo + e_count - 1 at
+  // desc_base + e - e_lo and the shared expert (global id E) right after them
+  int e_lo, e_count;
+  // epi 2 (expert-parallel combine into the tensor-parallel all-reduce): tokens T, receive tables
+  int T;
+  unsigned long long* const* push_recv;
+  const int* push_epoch;
+  int push_n;
 };
 void moe_mixed_gemv_launch(int epi, const MoeMixedArgs& a, int max_active, cudaStream_t s, bool pdl);
 void moe_active_launch(const int* counts, int E, int* active, int* n_active, cudaStream_t s, bool pdl);

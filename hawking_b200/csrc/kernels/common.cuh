@@ -41,6 +41,14 @@ __device__ __forceinline__ void set_error(int* status, int code) {
 #define HK_GUARD(cond, status)
 #endif
 
+// Packed greedy key: order-preserving bits of the value in the high word, the complement of the
+// index in the low word (so the lowest index wins a tie); 0 means "no value".
+__device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
+  uint32_t u = __float_as_uint(v);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((unsigned long long)u << 32) | (0xFFFFFFFFu - (uint32_t)idx);
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

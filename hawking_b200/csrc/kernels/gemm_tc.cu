@@ -1,5 +1,6 @@
 // Tensor-core dequant GEMM (K1, batch >= 16 and prefill): Y[M, N] (+)= X[M, K] . W[N, K]^T with W
-// in GGUF Q4_K, X bf16, fp32 accumulation in TMEM via tcgen05.mma (kind::f16, M=128, N=BN, K=16).
+// in GGUF Q4_K, X bf16, fp32 accumulation in TMEM via tcgen05.mma (kind::f16, M=128, N=BN, K=16),
+// BN in {32, 64, 128, 256} (256 for prefill-sized M: the dequantised tile serves twice the tokens).
 //
 // One CTA owns a 128-row weight tile and a BN-token tile over a K range (split-K across
 // blockIdx.z, reduced with fp32 atomics). Warp roles:
@@ -35,7 +36,7 @@ using namespace sm100;
 constexpr int BM = 128;        // weight rows per tile (UMMA M)
 constexpr int BK = 128;        // K per stage (half a Q4_K super-block)
 constexpr int DA = 2;          // A/X stages
-constexpr int DR = 4;          // raw weight stages
+constexpr int DR_MAX = 4;      // raw weight stages (2 at BN = 256, where shared memory is short)
 constexpr int kThreads = 384;
 constexpr int kDequantWarp0 = 4;
 constexpr int kDequantWarps = 8;
@@ -46,6 +47,7 @@ constexpr uint32_t RAW_QS = BM * 64;        // 8 KB
 
 template <int BN>
 struct Layout {
+  static constexpr int DR = BN >= 256 ? 2 : DR_MAX;
   static constexpr uint32_t X_ATOM = BN * 128;
   static constexpr uint32_t X_STAGE = 2 * X_ATOM;
   static constexpr uint32_t off_a = 0;
@@ -55,6 +57,7 @@ struct Layout {
   static constexpr uint32_t off_bar = off_qs + DR * RAW_QS;
   static constexpr uint32_t n_bars = 2 * DR + 2 * DA + 1;
   static constexpr uint32_t total = off_bar + n_bars * 8 + 16 + 1024;  // + alignment slack
+  static_assert(total <= 232448, "tc_gemm: shared memory over the 227 KB per-CTA limit");
 };
 
 struct TcArgs {
@@ -94,10 +97,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::off_bar);
   uint64_t* raw_full = bars;
-  uint64_t* raw_empty = bars + DR;
-  uint64_t* a_full = bars + 2 * DR;
-  uint64_t* a_empty = bars + 2 * DR + DA;
-  uint64_t* acc_full = bars + 2 * DR + 2 * DA;
+  uint64_t* raw_empty = bars + L::DR;
+  uint64_t* a_full = bars + 2 * L::DR;
+  uint64_t* a_empty = bars + 2 * L::DR + DA;
+  uint64_t* acc_full = bars + 2 * L::DR + 2 * DA;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::n_bars);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -108,7 +111,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t tmem_cols = BN < 32 ? 32 : BN;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < DR; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], kDequantWarps); }
+    for (int i = 0; i < L::DR; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], kDequantWarps); }
     for (int i = 0; i < DA; ++i) { mbar_init(&a_full[i], kDequantWarps + 1); mbar_init(&a_empty[i], 1); }
     mbar_init(acc_full, 1);
     fence_barrier_init();
@@ -127,8 +130,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---- raw Q4_K producer ----
       int issued = 0;
       for (int i = 0; i < nst; ++i) {
-        const int slot = i % DR;
-        if (!mbar_wait(&raw_empty[slot], ((i / DR) & 1) ^ 1, a.status)) break;
+        const int slot = i % L::DR;
+        if (!mbar_wait(&raw_empty[slot], ((i / L::DR) & 1) ^ 1, a.status)) break;
         const int gs = s0 + i, sb = gs >> 1, h = gs & 1;
         mbar_arrive_expect_tx(&raw_full[slot], RAW_HDR + RAW_QS);
         tma_load_2d(smem + L::off_hdr + slot * RAW_HDR, &tm_hdr, sb * 16, n0, &raw_full[slot]);
@@ -136,7 +139,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++issued;
       }
       // Drain: every issued copy has landed before the CTA may exit.
-      for (int i = max(0, issued - DR); i < issued; ++i) mbar_wait(&raw_full[i % DR], (i / DR) & 1, nullptr, 1u << 22);
+      for (int i = max(0, issued - L::DR); i < issued; ++i) mbar_wait(&raw_full[i % L::DR], (i / L::DR) & 1, nullptr, 1u << 22);
     } else if (warp == 1 && lane == 0) {
       // ---- activation producer ----
       int issued = 0;
@@ -181,8 +184,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int t = (warp - kDequantWarp0) * 32 + lane;
       const int r = t >> 1, c = t & 1;
       for (int i = 0; i < nst; ++i) {
-        const int rs = i % DR, as = i % DA;
-        const bool ok_raw = __shfl_sync(0xffffffffu, mbar_wait(&raw_full[rs], (i / DR) & 1, a.status), 0);
+        const int rs = i % L::DR, as = i % DA;
+        const bool ok_raw = __shfl_sync(0xffffffffu, mbar_wait(&raw_full[rs], (i / L::DR) & 1, a.status), 0);
         if (!ok_raw) break;
         const uint4 hdr = *reinterpret_cast<const uint4*>(smem + L::off_hdr + rs * RAW_HDR + r * 16);
         const uint4 q0 = *reinterpret_cast<const uint4*>(smem + L::off_qs + rs * RAW_QS + r * 64 + c * 32);
@@ -330,7 +333,8 @@ void tc_gemm_launch(const TcGemmArgs& g, cudaStream_t s) {
     case 32: launch_bn<32>(g, s); break;
     case 64: launch_bn<64>(g, s); break;
     case 128: launch_bn<128>(g, s); break;
-    default: throw std::runtime_error("tc_gemm: bn must be 32, 64 or 128");
+    case 256: launch_bn<256>(g, s); break;
+    default: throw std::runtime_error("tc_gemm: bn must be 32, 64, 128 or 256");
   }
 }
 

@@ -68,14 +68,6 @@ template <> struct Fmt<WF_Q5_0> {
   }
 };
 
-// Packed greedy key: order-preserving bits of the value in the high word, the complement of the
-// index in the low word (so the lowest index wins a tie); 0 means "no value".
-__device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
-  uint32_t u = __float_as_uint(v);
-  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-  return ((unsigned long long)u << 32) | (0xFFFFFFFFu - (uint32_t)idx);
-}
-
 // The activation source of one launch, resolved to plain pointers (global or shared memory).
 struct XSrc {
   const int8_t* q;

@@ -27,6 +27,7 @@
 
 #include "api.h"
 #include "qformats.cuh"
+#include "tp.cuh"
 
 namespace hk {
 
@@ -150,10 +151,19 @@ __global__ void __launch_bounds__(256) mixed_gemv_kernel(MixedGemvArgs a) {
       if (n < a.N) {
         float v = mixed_row_dot(t0, n, a.K, xq, xd, xs) * a.alpha;
         if (a.gate_logit) v *= 1.f / (1.f + __expf(-a.gate_logit[(int64_t)b * a.gate_stride]));
-        if (lane == 0) {
+        if constexpr (EPI == EPI_PUSH) {
+          // row-parallel projection: this rank's partial to every rank (lanes spread the peers)
+          const uint32_t flag = (uint32_t)*a.push_epoch;
+          for (int p = lane; p < a.push_n; p += 32) ll_store(a.push_recv[p] + (int64_t)b * a.N + n, __float_as_uint(v), flag);
+        } else if (lane == 0) {
           float* y = a.y + (int64_t)b * a.y_stride + n;
           if constexpr (EPI == EPI_RESID) *y += v;
           else *y = v;
+          if constexpr (EPI == EPI_STORE) {
+            if (a.argmax_slots)
+              atomicMax(a.argmax_slots + (int64_t)b * kArgmaxSlots + (n % kArgmaxSlots),
+                        argmax_key(v, (int)(n + a.argmax_offset)));
+          }
         }
       }
     }
@@ -168,12 +178,23 @@ void mixed_gemv_launch(int epi, const MixedGemvArgs& a, cudaStream_t s, bool pdl
     launch(mixed_gemv_kernel<EPI_SWIGLU_Q8>, dim3(a.N / 32), dim3(256), 0, s, pdl, a);
   } else if (epi == EPI_RESID) {
     launch(mixed_gemv_kernel<EPI_RESID>, dim3((a.N + 7) / 8), dim3(256), 0, s, pdl, a);
+  } else if (epi == EPI_PUSH) {
+    if (!a.push_recv || !a.push_epoch || a.push_n <= 0 || a.nb > 8) throw std::runtime_error("mixed gemv push: peer tables, <= 8 rows");
+    launch(mixed_gemv_kernel<EPI_PUSH>, dim3((a.N + 7) / 8), dim3(256), 0, s, pdl, a);
   } else {
     launch(mixed_gemv_kernel<EPI_STORE>, dim3((a.N + 7) / 8), dim3(256), 0, s, pdl, a);
   }
 }
 
 // ---- routed experts ----------------------------------------------------------------------------
+// Table slot of global expert e: e itself, or under expert parallelism its local index (the
+// shared expert, global id E, follows the local experts).
+__device__ __forceinline__ int moe_desc_index(const MoeMixedArgs& a, int e) {
+  if (a.e_count == 0) return e;
+  const int l = e - a.e_lo;
+  return (l >= 0 && l < a.e_count) ? l : a.e_count;
+}
+
 // Grid (row blocks, active experts): blockIdx.y indexes a.active (experts with >= 1 pair).
 template <int EPI>
 __global__ void __launch_bounds__(256) moe_mixed_gemv_kernel(MoeMixedArgs a) {
@@ -184,8 +205,9 @@ __global__ void __launch_bounds__(256) moe_mixed_gemv_kernel(MoeMixedArgs a) {
   const int e = a.active[blockIdx.y];
   const int c = a.counts[e], off = a.offsets[e];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const MixedDesc tg = a.desc[a.desc_base0 + e];
-  const MixedDesc tu = EPI == 0 ? a.desc[a.desc_base1 + e] : tg;
+  const int di = moe_desc_index(a, e);
+  const MixedDesc tg = a.desc[a.desc_base0 + di];
+  const MixedDesc tu = EPI == 0 ? a.desc[a.desc_base1 + di] : tg;
   for (int p = 0; p < c; ++p) {
     const int sp = off + p;  // sorted pair index
     const int8_t* xq = a.xq + (int64_t)sp * a.K;
@@ -235,8 +257,49 @@ __global__ void __launch_bounds__(256) moe_mixed_gemv_kernel(MoeMixedArgs a) {
   pdl_launch();
 }
 
+// Expert-parallel combine (K4): the down projection of this rank's active experts for every
+// token, summed per token in registers (lane t of a warp holds token t) over the experts in
+// active-list order and their pairs in token order, then pushed to every rank's receive region as
+// flagged words: the combine IS this rank's contribution to the layer's all-reduce, and the next
+// RMSNorm (tp_allreduce_rmsnorm_q8) adds the ranks' contributions into the residual. One warp per
+// hidden row, no atomics, no partial buffer. Tokens were never dispatched: the hidden state is
+// replicated on every rank by the attention all-reduce, so each rank reads its pairs' rows locally.
+__global__ void __launch_bounds__(256) moe_mixed_combine_push_kernel(MoeMixedArgs a) {
+  pdl_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = blockIdx.x * 8 + warp;
+  const int na = *a.n_active;
+  float acc = 0.f;
+  for (int i = 0; i < na; ++i) {
+    const int e = a.active[i];
+    const int c = a.counts[e], off = a.offsets[e];
+    const MixedDesc t = a.desc[a.desc_base0 + moe_desc_index(a, e)];
+    for (int p = 0; p < c; ++p) {
+      const int sp = off + p;
+      const float v = mixed_row_dot(t, n, a.K, a.xq + (int64_t)sp * a.K, a.xd + (int64_t)sp * (a.K / 32),
+                                    a.xs + (int64_t)sp * (a.K / 32));
+      const int pair = a.sorted[sp];
+      const bool routed = pair < a.routed_pairs;
+      const int tok = routed ? pair / a.k : pair - a.routed_pairs;
+      if (lane == tok) acc += (routed ? a.route_w[pair] : 1.f) * v;
+    }
+  }
+  pdl_launch();
+  if (lane < a.T) {
+    const uint32_t flag = (uint32_t)*a.push_epoch;
+    for (int p = 0; p < a.push_n; ++p) ll_store(a.push_recv[p] + (int64_t)lane * a.N + n, __float_as_uint(acc), flag);
+  }
+}
+
 void moe_mixed_gemv_launch(int epi, const MoeMixedArgs& a, int max_active, cudaStream_t s, bool pdl) {
   if (a.K % 32) throw std::runtime_error("moe mixed gemv: K must be a multiple of 32");
+  if (epi == 2) {
+    if (a.N % 8) throw std::runtime_error("moe combine push: hidden must be a multiple of 8");
+    if (!a.push_recv || !a.push_epoch || a.push_n <= 0 || a.T < 1 || a.T > 8)
+      throw std::runtime_error("moe combine push: peer tables and 1..8 tokens required");
+    launch(moe_mixed_combine_push_kernel, dim3(a.N / 8), dim3(256), 0, s, pdl, a);
+    return;
+  }
   if (epi == 0) {
     if (a.N % 32) throw std::runtime_error("moe mixed gemv: expert FFN width must be a multiple of 32");
     launch(moe_mixed_gemv_kernel<0>, dim3(a.N / 32, max_active), dim3(256), 0, s, pdl, a);

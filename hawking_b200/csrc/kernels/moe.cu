@@ -17,6 +17,7 @@
 // qwen80_postnorm_router_top10 / qwen80_all_ten_routed_expert_wave (512-way expert table).
 #include "api.h"
 #include "qformats.cuh"
+#include "tp.cuh"
 
 namespace hk {
 
@@ -260,9 +261,11 @@ __global__ void __launch_bounds__(256) moe_route_kernel(MoeRouteArgs a) {
   if (tid == 0) {
     off[0] = 0;
     int n = 0;
+    const int lo = a.e_lo, hi = a.e_hi > 0 ? a.e_hi : E;
     for (int e = 0; e < E1; ++e) {
       off[e + 1] = off[e] + cnt[e];
-      if (cnt[e] > 0) a.active[n++] = e;
+      // expert parallelism: only this rank's experts (and the shared one, when appended) run here
+      if (cnt[e] > 0 && ((e >= lo && e < hi) || e == E)) a.active[n++] = e;
     }
     *a.n_active = n;
     *a.counter = 0;  // ready for the next launch
@@ -272,10 +275,10 @@ __global__ void __launch_bounds__(256) moe_route_kernel(MoeRouteArgs a) {
     a.counts[e] = cnt[e];
     a.offsets[e] = off[e];
   }
-  if (tid < E) {
-    int pos = off[tid];
+  for (int e = tid; e < E; e += blockDim.x) {  // stable: the pairs of one expert keep token order
+    int pos = off[e];
     for (int p = 0; p < P; ++p)
-      if (a.ids[p] == tid) a.sorted[pos++] = p;
+      if (a.ids[p] == e) a.sorted[pos++] = p;
   }
   if (a.shared)
     for (int t = tid; t < T; t += blockDim.x) a.sorted[P + t] = P + t;
@@ -314,8 +317,7 @@ __global__ void __launch_bounds__(1024) moe_align_kernel(MoeAlignArgs a) {
     a.offsets[e] = off[e];
   }
   // Stable placement: pairs of one expert keep token order (serial per expert bucket).
-  if (tid < a.E) {
-    const int e = tid;
+  for (int e = tid; e < a.E; e += blockDim.x) {
     int pos = off[e];
     for (int p = 0; p < P; ++p)
       if (a.ids[p] == e) a.sorted[pos++] = p;
@@ -399,7 +401,7 @@ __device__ __forceinline__ void m_chunk(const MoeGemvArgs& a, int e, int p0, flo
     for (int r = 0; r < 4; ++r) {
       const int n = blockIdx.x * 32 + warp * 4 + r;
       float g[NB], u[NB];
-      const int64_t row = (int64_t)e * a.N + n;
+      const int64_t row = (int64_t)(e - a.e_lo) * a.N + n;
       m_row_dot<FMT, NB>(a.w0, row, n_units, q, d, s, a.K, g);
       m_row_dot<FMT, NB>(a.w1, row, n_units, q, d, s, a.K, u);
       if (lane == 0)
@@ -425,7 +427,7 @@ __device__ __forceinline__ void m_chunk(const MoeGemvArgs& a, int e, int p0, flo
   } else {
     const int n = blockIdx.x * 8 + warp;
     float acc[NB];
-    m_row_dot<FMT, NB>(a.w0, (int64_t)e * a.N + n, n_units, q, d, s, a.K, acc);
+    m_row_dot<FMT, NB>(a.w0, (int64_t)(e - a.e_lo) * a.N + n, n_units, q, d, s, a.K, acc);
     if (lane < NB) {
       float v = acc[0];
 #pragma unroll
@@ -442,7 +444,7 @@ template <int FMT, int EPI>
 __global__ void __launch_bounds__(256) moe_gemv_kernel(MoeGemvArgs a) {
   __shared__ float hbuf[8][32];
   pdl_wait();
-  const int e = blockIdx.y;
+  const int e = a.e_lo + (int)blockIdx.y;  // global expert id (weights stacked from e_lo)
   const int c = a.counts[e];
   if (c == 0) { pdl_launch(); return; }
   const int off = a.offsets[e];
@@ -462,6 +464,38 @@ __global__ void __launch_bounds__(256) moe_gemv_kernel(MoeGemvArgs a) {
   pdl_launch();
 }
 
+// Expert-parallel combine (K4) for GGUF-format experts: one warp per hidden row sums, per token,
+// the route-weighted down projections of this rank's experts (experts in order, pairs in token
+// order; lane t holds token t) and pushes the sums to every rank's receive region as flagged
+// words, which the next RMSNorm (tp_allreduce_rmsnorm_q8) adds into the residual. The hidden
+// state is replicated by the attention all-reduce, so nothing is dispatched: each rank's experts
+// read their pairs' gathered rows locally.
+template <int FMT>
+__global__ void __launch_bounds__(256) moe_combine_push_kernel(MoeGemvArgs a, int n_local) {
+  pdl_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = blockIdx.x * 8 + warp;
+  const int n_units = a.K / 128;
+  float acc = 0.f;
+  for (int le = 0; le < n_local; ++le) {
+    const int e = a.e_lo + le;
+    const int c = a.counts[e], off = a.offsets[e];
+    for (int p = 0; p < c; ++p) {
+      const int sp = off + p;
+      float v[1];
+      m_row_dot<FMT, 1>(a.w0, (int64_t)le * a.N + n, n_units, a.xq + (int64_t)sp * a.K, a.xd + (int64_t)sp * (a.K / 32),
+                        a.xs + (int64_t)sp * (a.K / 32), a.K, v);
+      const int pair = a.sorted[sp];
+      if (lane == pair / a.k) acc += a.route_w[pair] * v[0];
+    }
+  }
+  pdl_launch();
+  if (lane < a.T) {
+    const uint32_t flag = (uint32_t)*a.push_epoch;
+    for (int p = 0; p < a.push_n; ++p) ll_store(a.push_recv[p] + (int64_t)lane * a.N + n, __float_as_uint(acc), flag);
+  }
+}
+
 template <int EPI>
 static void moe_gemv_fmt(int fmt, const MoeGemvArgs& a, cudaStream_t s, bool pdl) {
   const int rows_per_cta = EPI == 0 ? 32 : 8;
@@ -477,6 +511,20 @@ static void moe_gemv_fmt(int fmt, const MoeGemvArgs& a, cudaStream_t s, bool pdl
 
 void moe_gemv_launch(int fmt, int epi, const MoeGemvArgs& a, cudaStream_t s, bool pdl) {
   if (a.K % 128) throw std::runtime_error("moe_gemv: K must be a multiple of 128");
+  if (epi == 2) {
+    if (a.N % 8) throw std::runtime_error("moe combine push: hidden must be a multiple of 8");
+    if (!a.push_recv || !a.push_epoch || a.push_n <= 0 || a.T < 1 || a.T > 8)
+      throw std::runtime_error("moe combine push: peer tables and 1..8 tokens required");
+    const dim3 grid(a.N / 8);
+    switch (fmt) {
+      case WF_Q4_K: launch(moe_combine_push_kernel<WF_Q4_K>, grid, dim3(256), 0, s, pdl, a, a.E); break;
+      case WF_Q4_0: launch(moe_combine_push_kernel<WF_Q4_0>, grid, dim3(256), 0, s, pdl, a, a.E); break;
+      case WF_Q8_0: launch(moe_combine_push_kernel<WF_Q8_0>, grid, dim3(256), 0, s, pdl, a, a.E); break;
+      case WF_Q6_K: launch(moe_combine_push_kernel<WF_Q6_K>, grid, dim3(256), 0, s, pdl, a, a.E); break;
+      default: throw std::runtime_error("moe combine push: unsupported weight format");
+    }
+    return;
+  }
   if (epi == 0) {
     if (a.N % 32) throw std::runtime_error("moe_gemv: expert FFN width must be a multiple of 32");
     moe_gemv_fmt<0>(fmt, a, s, pdl);

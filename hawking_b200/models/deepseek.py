@@ -12,6 +12,14 @@ block scales (K1 fp8 path of the mixed GEMV kernels); W_UK / W_UV are kept in bf
 Decode runs rows <= 8 through the GEMV path; prompts are fed through the same path in chunks of up
 to 8 tokens of one sequence (the latent cache makes multi-row prefill exact).
 
+Across the GPUs of a node (``tp`` given, weights from ``parallel.ep``): attention is tensor
+parallel over heads (q_b, W_UK, W_UV and the output projection split by head; q_a / kv_a and the
+latent cache replicated), the dense FFN layers split by FFN row, the routed experts expert
+parallel (each rank holds E / N whole experts; the shared expert runs on rank l mod N), and the
+LM head split by vocabulary row. Every row-parallel result (output projection, FFN down, the
+experts' combine) is pushed from its kernel's epilogue into every rank's receive region, and the
+next RMSNorm sums the ranks (``csrc/kernels/tp.cu``); greedy sampling reduces per-rank keys.
+
 Parity: crates/hawking-core/src/model/deepseek_v2.rs:72-158 (config: q_lora, kv_lora 512, rope 64,
 nope 128, v 128, routed + shared experts, first_k_dense), :2170 (forward_token), crates/hawking-core/
 src/attn.rs:185 (mla_decode_step), crates/hawking-core/src/moe.rs:24 (top-k gate),
@@ -28,7 +36,7 @@ import torch
 from .. import ops
 from .._ext import kernels
 from ..ops import Q8Act, QWeight
-from ..ops.mixed import MixedTable, MixedWeight, mixed_gemv, mixed_gemv_swiglu
+from ..ops.mixed import MixedTable, MixedWeight, mixed_gemv, mixed_gemv_push, mixed_gemv_swiglu
 from .config import ModelConfig
 
 LAT, ROPE = 512, 64
@@ -46,6 +54,7 @@ class DSLayer:
     idx: Dict[str, int] = field(default_factory=dict)
     router: Optional[torch.Tensor] = None
     router_bias: Optional[torch.Tensor] = None
+    shared_here: bool = True            # expert parallel: this rank runs the layer's shared expert
 
 
 @dataclass
@@ -55,6 +64,8 @@ class DSWeights:
     out_norm: torch.Tensor
     layers: List[DSLayer]
     lm_head: int
+    e_lo: int = 0                       # expert parallel: this rank's routed experts are
+    e_count: int = 0                    # e_lo .. e_lo + e_count - 1 (0: all of them)
 
     @property
     def nbytes(self) -> int:
@@ -128,10 +139,12 @@ def random_deepseek_weights(cfg: ModelConfig, device, seed: int = 0, std: float 
 class DeepSeekModel:
     """Decode forward over static buffers (rows <= 8)."""
 
-    def __init__(self, cfg: ModelConfig, w: DSWeights, kv, max_rows: int = 8, device="cuda"):
+    def __init__(self, cfg: ModelConfig, w: DSWeights, kv, max_rows: int = 8, device="cuda", tp=None):
         """``kv``: PagedKVCache-like object with ``latent[l]`` [num_blocks, block_size, 576] bf16
-        per layer, ``block_tables``, ``bm`` (see models.deepseek.LatentCache)."""
+        per layer, ``block_tables``, ``bm`` (see models.deepseek.LatentCache). With ``tp``
+        (parallel.tp.TPComm), ``cfg`` is this rank's shard (heads and dense FFN divided)."""
         self.cfg, self.w, self.kv, self.dev = cfg, w, kv, torch.device(device)
+        self.tp = tp
         self.max_rows = R = min(max_rows, 8)
         dev = self.dev
         H, nh = cfg.hidden, cfg.n_heads
@@ -172,6 +185,9 @@ class DeepSeekModel:
         self.rope = ops.rope_table(cfg.max_ctx, ROPE, cfg.rope_theta, None, dev)
         self.scale = 1.0 / math.sqrt(nope + rd)
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        if tp is not None:
+            self.x2 = torch.zeros(R, H, device=dev)  # second residual buffer of the push all-reduce
+            self.argmax_slots = torch.zeros(R, ops.ARGMAX_SLOTS, dtype=torch.int64, device=dev)
         self._graphs = {}
         self.launches_per_graph = 0
 
@@ -196,27 +212,43 @@ class DeepSeekModel:
         K.mla_decode(self.q_lat[:rows], self.q_pe[:rows], kv.latent[l], kv.block_tables, inp.row_seq[:rows],
                      inp.row_ctx[:rows], self.scale, self.num_splits(rows), self.o_lat[:rows], self.status, ops.PDL)
         K.mla_out(self.o_lat[:rows], L.w_uv, self.attq.q[:rows], self.attq.d[:rows], self.attq.s[:rows], ops.PDL)
-        mixed_gemv(t, L.idx["o"], self.attq.view(rows), self.x[:rows], residual=True)
+        if self.tp is not None:
+            mixed_gemv_push(t, L.idx["o"], self.attq.view(rows), self.tp, 2 * l)
+        else:
+            mixed_gemv(t, L.idx["o"], self.attq.view(rows), self.x[:rows], residual=True)
 
-    def _ffn(self, L, rows):
-        cfg, t = self.cfg, self.w.table
+    def _ffn(self, L, rows, site: int = -1):
+        """FFN / MoE of one layer; under tensor parallelism (``site`` >= 0) the result is pushed to
+        every rank's receive region of ``site`` instead of added to the residual."""
+        cfg, t, tp = self.cfg, self.w.table, self.tp
         xa = self.xa.view(rows)
         if L.dense:
             h = self.h.view(rows)
             mixed_gemv_swiglu(t, L.idx["g"], L.idx["u"], xa, h)
-            mixed_gemv(t, L.idx["d"], h, self.x[:rows], residual=True)
+            if tp is not None:
+                mixed_gemv_push(t, L.idx["d"], h, tp, site)
+            else:
+                mixed_gemv(t, L.idx["d"], h, self.x[:rows], residual=True)
             return
         E, k, H, F = cfg.n_experts, cfg.top_k, cfg.hidden, cfg.expert_ffn
-        fold = self.fold_shared and L.idx["sg"] == L.idx["eg"] + E and L.idx["su"] == L.idx["eu"] + E and \
-            L.idx["sd"] == L.idx["ed"] + E
+        ne = self.w.e_count or E  # routed experts in this rank's table
+        e_lo = self.w.e_lo
+        fold = self.fold_shared and L.shared_here and L.idx.get("sg") == L.idx["eg"] + ne and \
+            L.idx.get("su") == L.idx["eu"] + ne and L.idx.get("sd") == L.idx["ed"] + ne
+        if tp is not None and L.shared_here and not fold:
+            raise NotImplementedError("expert parallel: the shared expert must have the routed experts' shape")
         K = kernels()
         if self.fused_route:
-            # one launch: router GEMV, top-k, sort by expert, active list; experts read token rows
+            # one launch: router GEMV, top-k, sort by expert, active list (this rank's experts only
+            # under expert parallelism); experts read token rows
             ops.moe_route(L.router, xa, k, 1, L.router_bias, cfg.n_groups, cfg.topk_groups, cfg.norm_topk,
                           cfg.routed_scale, self.rlog[:rows], self.ids[:rows], self.rw[:rows], self.counts,
-                          self.offsets, self.sorted, self.active, self.n_active, fold, self.route_counter)
+                          self.offsets, self.sorted, self.active, self.n_active, fold, self.route_counter,
+                          e_lo=e_lo, e_hi=e_lo + ne if self.w.e_count else 0)
             gin = xa
         else:
+            if self.w.e_count:
+                raise NotImplementedError("expert parallel needs the fused routing kernel")
             ops.router_logits(L.router, xa, self.rlog[:rows])
             ops.moe_topk(self.rlog[:rows], L.router_bias, k, 1, cfg.n_groups, cfg.topk_groups, cfg.norm_topk,
                          cfg.routed_scale, self.ids[:rows], self.rw[:rows])
@@ -225,19 +257,29 @@ class DeepSeekModel:
             K.moe_active(self.counts, self.active, self.n_active, ops.PDL)
             gin = self.gx
         ops.launches.add(2)
-        na = min(E, rows * k) + (1 if fold else 0)
+        na = min(ne, rows * k) + (1 if fold else 0)
+        ep = dict(e_lo=e_lo, e_count=self.w.e_count)
         K.moe_mixed_gemv(0, t.descs, L.idx["eg"], L.idx["eu"], F, H, k, self.counts, self.offsets, self.sorted,
                          self.active, self.n_active, na, gin.q, gin.d, gin.s, self.hx.q, self.hx.d,
-                         self.hx.s, None, None, ops.PDL, rows * k, self.fused_route)
+                         self.hx.s, None, None, ops.PDL, rows * k, self.fused_route, **ep)
+        if tp is not None:
+            # expert-parallel combine: per-token sum over this rank's experts, pushed to every rank
+            K.moe_mixed_gemv(2, t.descs, L.idx["ed"], L.idx["ed"], H, F, k, self.counts, self.offsets, self.sorted,
+                             self.active, self.n_active, na, self.hx.q, self.hx.d, self.hx.s, None, None, None,
+                             None, self.rw[:rows].reshape(-1), ops.PDL, rows * k, T=rows,
+                             push_table=tp.push_recv[site], push_epoch=tp.epoch, **ep)
+            return
         K.moe_mixed_gemv(1, t.descs, L.idx["ed"], L.idx["ed"], H, F, k, self.counts, self.offsets, self.sorted,
                          self.active, self.n_active, na, self.hx.q, self.hx.d, self.hx.s, None, None, None,
-                         self.x[:rows], self.rw[:rows].reshape(-1), ops.PDL, rows * k)
+                         self.x[:rows], self.rw[:rows].reshape(-1), ops.PDL, rows * k, **ep)
         if not fold:
             hs = self.hs.view(rows)
             mixed_gemv_swiglu(t, L.idx["sg"], L.idx["su"], xa, hs)
             mixed_gemv(t, L.idx["sd"], hs, self.x[:rows], residual=True)
 
     def forward(self, rows: int, sample: str = "greedy", advance: bool = False):
+        if self.tp is not None:
+            return self._forward_tp(rows, sample, advance)
         cfg, w, inp = self.cfg, self.w, self.inp
         ops.embed(w.embed, inp.ids[:rows], self.x[:rows])
         for l, L in enumerate(w.layers):
@@ -249,6 +291,35 @@ class DeepSeekModel:
         mixed_gemv(w.table, w.lm_head, self.xa.view(rows), self.logits[:rows])
         if sample == "greedy":
             ops.argmax(self.logits[:rows], self.next_ids[:rows])
+        if advance:
+            ops.advance(inp.ids, self.next_ids, inp.positions, inp.row_ctx, rows)
+
+    def _forward_tp(self, rows: int, sample: str, advance: bool):
+        """Tensor/expert-parallel decode forward: two push all-reduce sites per layer (attention
+        output, FFN / expert combine), each consumed by the next RMSNorm on every rank."""
+        cfg, w, inp, tp = self.cfg, self.w, self.inp, self.tp
+        if rows > 8:
+            raise RuntimeError("tensor-parallel decode takes at most 8 rows")
+        ops.tp_begin(tp)
+        xa_res, xb_res = self.x[:rows], self.x2[:rows]
+        ops.embed(w.embed, inp.ids[:rows], xa_res)
+        ops.rmsnorm_q8(xa_res, w.layers[0].attn_norm, cfg.eps, self.xa.view(rows))
+        for l, L in enumerate(w.layers):
+            self._attention(l, L, rows)
+            ops.tp_allreduce_rmsnorm_q8(tp, 2 * l, xa_res, xb_res, L.ffn_norm, cfg.eps, self.xa.view(rows))
+            self._ffn(L, rows, site=2 * l + 1)
+            nxt = w.layers[l + 1].attn_norm if l + 1 < len(w.layers) else w.out_norm
+            ops.tp_allreduce_rmsnorm_q8(tp, 2 * l + 1, xb_res, xa_res, nxt, cfg.eps, self.xa.view(rows))
+        # the last all-reduce left norm(x) in self.xa; this rank's vocabulary slice of the LM head
+        head = w.table.weights[w.lm_head]
+        if sample == "greedy":
+            mixed_gemv(w.table, w.lm_head, self.xa.view(rows), self.logits[:rows],
+                       argmax_slots=self.argmax_slots[:rows], argmax_offset=tp.rank * head.N)
+            ops.tp_argmax(tp, self.argmax_slots, rows, self.next_ids)
+        elif sample == "none":
+            mixed_gemv(w.table, w.lm_head, self.xa.view(rows), self.logits[:rows])
+        else:
+            raise NotImplementedError("tensor-parallel sampling: greedy only")
         if advance:
             ops.advance(inp.ids, self.next_ids, inp.positions, inp.row_ctx, rows)
 

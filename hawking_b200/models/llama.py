@@ -170,20 +170,31 @@ class StepInputs:
         self.slots = torch.zeros(max_rows, dtype=torch.int32, device=device)
         self.row_seq = torch.zeros(max_rows, dtype=torch.int32, device=device)
         self.row_ctx = torch.ones(max_rows, dtype=torch.int32, device=device)
-        # Packed host staging: one H2D copy per step.
+        # Packed host staging: one H2D copy per step, from a ring of two pinned buffers. A buffer
+        # is rewritten only after the copy that last read it has run (its event), so a host that
+        # runs ahead of the GPU cannot change the inputs of a step that is still queued.
         self._packed_dev = torch.zeros(5, max_rows, dtype=torch.int32, device=device)
-        self._packed_host = torch.zeros(5, max_rows, dtype=torch.int32).pin_memory()
+        self._host_ring = [torch.zeros(5, max_rows, dtype=torch.int32).pin_memory() for _ in range(2)]
+        self._host_done = [None, None]
+        self._turn = 0
         self.ids, self.positions, self.slots, self.row_seq, self.row_ctx = self._packed_dev.unbind(0)
 
     def upload(self, ids, positions, slots, row_seq, row_ctx):
         n = len(ids)
-        h = self._packed_host
+        i = self._turn
+        self._turn ^= 1
+        if self._host_done[i] is not None:
+            self._host_done[i].synchronize()
+        h = self._host_ring[i]
         h[0, :n] = torch.as_tensor(ids, dtype=torch.int32)
         h[1, :n] = torch.as_tensor(positions, dtype=torch.int32)
         h[2, :n] = torch.as_tensor(slots, dtype=torch.int32)
         h[3, :n] = torch.as_tensor(row_seq, dtype=torch.int32)
         h[4, :n] = torch.as_tensor(row_ctx, dtype=torch.int32)
-        self._packed_dev.copy_(h, non_blocking=True)
+        self._packed_dev[:, :n].copy_(h[:, :n], non_blocking=True)
+        ev = self._host_done[i] or torch.cuda.Event()
+        ev.record()
+        self._host_done[i] = ev
         return n * 5 * 4
 
 

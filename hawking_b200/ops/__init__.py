@@ -205,7 +205,8 @@ def tc_gemm(w: QWeight, x: torch.Tensor, y: torch.Tensor, status: torch.Tensor, 
     so unless ``atomic`` (residual add) the caller passes a zeroed ``y`` and ``y_zeroed=True``."""
     M = x.shape[0]
     if bn == 0:
-        bn = 32 if M <= 32 else (64 if M <= 64 else 128)
+        # prefill-sized M: 256-token tiles halve the dequantisation per FLOP
+        bn = 32 if M <= 32 else (64 if M <= 64 else (128 if M < 192 else 256))
     if k_splits == 0 or k_splits is None:
         k_splits = kernels().tc_gemm_splits(w.N, M, w.K, bn, 148) if (atomic or y_zeroed) else 1
     launches.add()
@@ -231,12 +232,14 @@ def moe_topk(logits, bias, k: int, scoring: int, n_groups: int, topk_groups: int
 
 def moe_route(router, x: Q8Act, k: int, scoring: int, bias, n_groups: int, topk_groups: int, renorm: bool,
               scale: float, logits, ids, weights, counts, offsets, sorted_pairs, active, n_active, shared: bool,
-              counter):
+              counter, e_lo: int = 0, e_hi: int = 0):
     """Fused decode routing (one launch): router logits, top-k, the pairs sorted by expert (plus
-    the shared expert as expert E when ``shared``) and the list of experts with pairs."""
+    the shared expert as expert E when ``shared``) and the list of experts with pairs; under
+    expert parallelism only experts in [e_lo, e_hi) enter the active list."""
     launches.add()
     kernels().moe_route(router, x.q, x.d, k, scoring, bias, n_groups, topk_groups, renorm, scale, logits, ids,
-                        weights, counts, offsets, sorted_pairs, active, n_active, shared, counter, PDL)
+                        weights, counts, offsets, sorted_pairs, active, n_active, shared, counter, PDL,
+                        e_lo=e_lo, e_hi=e_hi)
 
 
 def moe_align(ids, E: int, x: Q8Act, counts, offsets, sorted_pairs, gathered: Q8Act, shared: bool = False):

@@ -161,6 +161,19 @@ class MixedWeight:
         return MixedWeight(self.kind, self.bits, self.group, count, self.K, self.codes[start:start + count],
                            self.scales[start:start + count], self.zero)
 
+    def cols(self, k0: int, k1: int) -> "MixedWeight":
+        """Columns [k0, k1) as a new contiguous tensor (whole scale groups: the row-parallel shard
+        of a tensor-parallel projection)."""
+        if k0 % self.group or k1 % self.group or k0 % 32 or k1 % 32:
+            raise ValueError("column slice must align to the scale groups and 32-element blocks")
+        b0, b1 = k0 * self.bits // 8, k1 * self.bits // 8
+        return MixedWeight(self.kind, self.bits, self.group, self.N, k1 - k0, self.codes[:, b0:b1].contiguous(),
+                           self.scales[:, k0 // self.group:k1 // self.group].contiguous(), self.zero)
+
+    def contiguous(self) -> "MixedWeight":
+        return MixedWeight(self.kind, self.bits, self.group, self.N, self.K, self.codes.contiguous(),
+                           self.scales.contiguous(), self.zero)
+
     @staticmethod
     def from_hq30(payload: np.ndarray, device) -> "MixedWeight":
         """A 2-D HQ30G1B1 (binary) or HQ30UQ4 (4-bit, zero point 8) payload whose groups tile the
@@ -199,12 +212,25 @@ class MixedTable:
         return sum(w.nbytes for w in self.weights)
 
 
-def mixed_gemv(table: MixedTable, i: int, x, y: torch.Tensor, residual: bool = False, gate_logit=None):
+def mixed_gemv(table: MixedTable, i: int, x, y: torch.Tensor, residual: bool = False, gate_logit=None,
+               argmax_slots=None, argmax_offset: int = 0):
+    """y (+)= W_i x; with ``argmax_slots`` (store only) every output also folds into the packed
+    greedy keys (index + ``argmax_offset``), as the GGUF GEMV's fused argmax."""
     from . import EPI_RESID, EPI_STORE, PDL, launches
     w = table.weights[i]
     launches.add()
     kernels().mixed_gemv(EPI_RESID if residual else EPI_STORE, table.descs, i, i, w.N, w.K, x.q, x.d, x.s, y, 1.0,
-                         None, None, None, PDL, gate_logit)
+                         None, None, None, PDL, gate_logit, argmax_slots=argmax_slots, argmax_offset=argmax_offset)
+
+
+def mixed_gemv_push(table: MixedTable, i: int, x, tp, site: int):
+    """Row-parallel projection: this rank's partial W_i x goes to every rank's receive region of
+    ``site`` (the tensor-parallel all-reduce push; the next RMSNorm sums the ranks)."""
+    from . import EPI_PUSH, PDL, launches
+    w = table.weights[i]
+    launches.add()
+    kernels().mixed_gemv(EPI_PUSH, table.descs, i, i, w.N, w.K, x.q, x.d, x.s, None, 1.0, None, None, None, PDL,
+                         None, push_table=tp.push_recv[site], push_epoch=tp.epoch)
 
 
 def mixed_gemv_swiglu(table: MixedTable, i_gate: int, i_up: int, x, out):

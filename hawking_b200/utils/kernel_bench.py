@@ -49,7 +49,7 @@ def _time_graph(fn, iters: int) -> float:
     return e0.elapsed_time(e1) * 1000.0 / iters
 
 
-def build_cases(dev: str = "cuda", ctx: int = 2048, rows: int = 1, only=None):
+def build_cases(dev: str = "cuda", ctx: int = 2048, rows: int = 1, only=None, bn: int = 0):
     from hawking_b200 import ops
     from hawking_b200.formats.ggml import GgmlType
     from hawking_b200.ops import Q8Act, QWeight
@@ -66,7 +66,7 @@ def build_cases(dev: str = "cuda", ctx: int = 2048, rows: int = 1, only=None):
 
     cases = {}
     if only is not None and all(c.startswith("tc_") or c == "attention_prefill" for c in only):
-        return _tc_cases(dev, ctx, rows, g, only)
+        return _tc_cases(dev, ctx, rows, g, only, bn)
     wo, wd, wqkv, wgu = copies((H, H)), copies((H, F)), copies((6144, H)), copies((F, H), (F, H))
     x = torch.randn(rows, H, device=dev)
     nw = torch.ones(H, device=dev)
@@ -117,7 +117,7 @@ def build_cases(dev: str = "cuda", ctx: int = 2048, rows: int = 1, only=None):
     return cases
 
 
-def _tc_cases(dev, ctx, rows, g, only):
+def _tc_cases(dev, ctx, rows, g, only, bn=0):
     """Tensor-core cases at ``rows`` tokens: the Q4_K dequant GEMMs of one layer and the causal
     prefill attention of one ``rows``-token chunk at the end of a ``ctx``-token prompt."""
     from hawking_b200 import ops
@@ -134,7 +134,8 @@ def _tc_cases(dev, ctx, rows, g, only):
         one = n * k * 144 // 256
         ws = [QWeight.random(GgmlType.Q4_K, n, k, 0.02, g, dev) for _ in range(max(1, -(-(256 << 20) // one)))]
         y = torch.zeros(rows, n, device=dev)
-        cases[name] = (lambda i, ws=ws, y=y, k=k: ops.tc_gemm(ws[i % len(ws)], x[:, :k], y, status, atomic=True),
+        cases[name] = (lambda i, ws=ws, y=y, k=k: ops.tc_gemm(ws[i % len(ws)], x[:, :k], y, status, atomic=True,
+                                                                         bn=bn),
                        one, 2.0 * rows * n * k)
     if "attention_prefill" in only:
         nblk = (ctx + BS - 1) // BS
@@ -159,8 +160,9 @@ def main(argv=None) -> None:
     ap.add_argument("--rows", type=int, default=1, help="decode batch (GEMV rows)")
     ap.add_argument("--ctx", type=int, default=2048)
     ap.add_argument("--plain", action="store_true", help="3 eager launches per case, no timing")
+    ap.add_argument("--bn", type=int, default=0, help="tensor-core token tile (0: the engine's choice)")
     args = ap.parse_args(argv)
-    cases = build_cases(ctx=args.ctx, rows=args.rows, only=args.case)
+    cases = build_cases(ctx=args.ctx, rows=args.rows, only=args.case, bn=args.bn)
     names = args.case or list(cases)
     for n in names:
         fn, nbytes = cases[n][:2]
@@ -172,7 +174,7 @@ def main(argv=None) -> None:
             print(json.dumps({"case": n, "plain": True}))
             continue
         us = _time_graph(fn, args.iters)
-        rec = {"case": n, "rows": args.rows, "us": round(us, 3), "gb_s": round(nbytes / us / 1e3, 1),
+        rec = {"case": n, "rows": args.rows, "bn": args.bn, "us": round(us, 3), "gb_s": round(nbytes / us / 1e3, 1),
                "bytes": int(nbytes)}
         if flops:
             rec["tflops"] = round(flops / us / 1e6, 1)

@@ -1,0 +1,81 @@
+"""Expert parallelism + tensor-parallel MLA on 2 GPUs (one process per GPU): the DeepSeek-style
+model sharded by ``parallel.ep`` (heads split, experts split 4 + 4, the shared expert on one rank
+per layer, experts' combine pushed from the down-projection epilogue) gives the single-GPU logits
+and greedy tokens.
+
+Runs only where at least two GPUs are visible."""
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, out_path):
+    import datetime
+
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        from hawking_b200.models.deepseek import DeepSeekModel, LatentCache, random_deepseek_weights
+        from hawking_b200.parallel.ep import local_deepseek_config, shard_deepseek_weights
+        from hawking_b200.parallel.tp import TPComm
+        from test_gpu_deepseek import tiny_cfg
+        cfg = tiny_cfg().with_(layers=4, first_dense_layers=1, n_heads=8, n_kv_heads=8)
+        w = random_deepseek_weights(cfg, dev, seed=3, std=0.05)  # same seed: identical on every rank
+        tp = TPComm(rank, world, 2 * cfg.layers, 8, cfg.hidden, dev)
+        kv = LatentCache(cfg.layers, 32, 16, 2, 16, dev)
+        m = DeepSeekModel(local_deepseek_config(cfg, world), shard_deepseek_weights(w, cfg, rank, world), kv,
+                          max_rows=8, device=dev, tp=tp)
+        toks = [5, 77, 300, 12, 9, 401, 256, 3, 44, 100, 7]
+        local = m.forward_tokens(toks, seq_id=1)[:, : cfg.vocab // world].contiguous()
+        ids = m.next_ids[: len(toks) - 8].clone()  # greedy ids of the last chunk (3 rows)
+        parts = [torch.empty_like(local) for _ in range(world)]
+        dist.all_gather(parts, local)
+        full = torch.cat(parts, 1)
+        all_ids = [torch.empty_like(ids) for _ in range(world)]
+        dist.all_gather(all_ids, ids)
+        tp.check()
+        if rank == 0:
+            kv1 = LatentCache(cfg.layers, 32, 16, 2, 16, dev)
+            ref_m = DeepSeekModel(cfg, w, kv1, max_rows=8, device=dev)
+            ref = ref_m.forward_tokens(toks, seq_id=1)
+            err = float((full - ref).abs().max() / ref.abs().max())
+            torch.save({"err": err, "ids": [t.tolist() for t in all_ids], "tp_argmax": full[8:].argmax(1).tolist(),
+                        "ref_ids": ref[8:].argmax(1).tolist(), "status": int(m.status.item())}, out_path)
+        torch.cuda.synchronize()
+        tp.close()
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep2_deepseek_matches_single_gpu(tmp_path):
+    import sys
+
+    import torch.multiprocessing as mp
+    sys.path.insert(0, os.path.dirname(__file__))
+    out = str(tmp_path / "ep.pt")
+    mp.spawn(_worker, args=(2, _free_port(), out), nprocs=2, join=True)
+    r = torch.load(out)
+    assert r["err"] < 0.02, r      # same kernels; the summation order (and so q8 rounding) differs
+    assert r["ids"][0] == r["ids"][1] == r["tp_argmax"], r  # vocabulary-parallel greedy is exact
+    assert sum(a == b for a, b in zip(r["ids"][0], r["ref_ids"])) >= 2, r
+    assert r["status"] == 0

@@ -25,7 +25,7 @@ def _check(y, ref):
     assert err <= 1.5e-2 * scale, (err, scale)
 
 
-@pytest.mark.parametrize("M,bn", [(1, 32), (16, 32), (64, 64), (100, 128), (130, 64)])
+@pytest.mark.parametrize("M,bn", [(1, 32), (16, 32), (64, 64), (100, 128), (130, 64), (300, 256), (256, 256)])
 def test_tc_gemm_store(M, bn):
     w, x, ref = _case(256, 1024, M, M + bn)
     y = torch.zeros(M, 256, device=DEV)
