@@ -24,13 +24,14 @@ void quantize(int64_t fmt, const Tensor& x, const std::vector<Tensor>& planes) {
   hk::quantize_launch((int)fmt, x.data_ptr<float>(), x.numel(), p[0], p[1], p[2], p[3], cur_stream());
 }
 void tc_gemm(int64_t fmt, const std::vector<Tensor>& planes, int64_t N, int64_t K, const Tensor& x, const Tensor& y,
-             bool atomic, bool y_zeroed, int64_t k_splits, int64_t bn, const Tensor& status, bool pdl) {
+             bool atomic, bool y_zeroed, int64_t k_splits, int64_t bn, const Tensor& status, bool pdl,
+             const c10::optional<Tensor>& h, bool persistent) {
   TORCH_CHECK(planes.size() == 2, "tc_gemm: Q4_K expects [quants, headers] planes");
   const Tensor& w = planes[0];
   const Tensor& wh = planes[1];
   TORCH_CHECK(w.is_cuda() && x.is_cuda() && y.is_cuda(), "tc_gemm: CUDA tensors required");
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.stride(-1) == 1, "tc_gemm: x must be bf16 rows");
-  TORCH_CHECK(y.scalar_type() == at::kFloat && y.stride(-1) == 1, "tc_gemm: y must be fp32 rows");
+  TORCH_CHECK(h.has_value() || (y.scalar_type() == at::kFloat && y.stride(-1) == 1), "tc_gemm: y must be fp32 rows");
   TORCH_CHECK(w.dim() == 2 && w.stride(-1) == 1, "tc_gemm: w must be [N, row_bytes]");
   TORCH_CHECK(status.scalar_type() == at::kInt, "tc_gemm: status must be int32");
   hk::TcGemmArgs g{};
@@ -44,7 +45,7 @@ void tc_gemm(int64_t fmt, const std::vector<Tensor>& planes, int64_t N, int64_t 
   g.x = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
   g.x_stride = x.stride(0);
   g.M = (int)x.size(0);
-  g.y = y.data_ptr<float>();
+  g.y = h.has_value() ? nullptr : y.data_ptr<float>();
   g.y_stride = y.stride(0);
   g.atomic = atomic;
   g.y_zeroed = y_zeroed;
@@ -52,6 +53,13 @@ void tc_gemm(int64_t fmt, const std::vector<Tensor>& planes, int64_t N, int64_t 
   g.bn = (int)bn;
   g.status = status.data_ptr<int>();
   g.pdl = pdl;
+  g.persistent = persistent ? 1 : 0;
+  if (h.has_value()) {
+    TORCH_CHECK(h->scalar_type() == at::kBFloat16 && h->stride(-1) == 1 && h->size(0) >= g.M && h->size(1) >= N / 2,
+                "tc_gemm swiglu: h must be bf16 [M, >= N / 2]");
+    g.h = reinterpret_cast<__nv_bfloat16*>(h->data_ptr());
+    g.h_stride = h->stride(0);
+  }
   const c10::cuda::CUDAGuard guard(x.device());
   hk::tc_gemm_launch(g, cur_stream());
 }
@@ -221,7 +229,7 @@ void register_more_kernels(py::module_& m) {
   m.def("quantize", &quantize, py::arg("fmt"), py::arg("x"), py::arg("planes"));
   m.def("tc_gemm", &tc_gemm, py::arg("fmt"), py::arg("planes"), py::arg("N"), py::arg("K"), py::arg("x"), py::arg("y"),
         py::arg("atomic"), py::arg("y_zeroed"), py::arg("k_splits"), py::arg("bn"), py::arg("status"),
-        py::arg("pdl") = false);
+        py::arg("pdl") = false, py::arg("h") = py::none(), py::arg("persistent") = false);
   m.def("tc_gemm_splits", &hk::tc_gemm_splits);
   m.def("router_logits", &router_logits, py::arg("w"), py::arg("xq"), py::arg("xd"), py::arg("logits"),
         py::arg("pdl") = false);

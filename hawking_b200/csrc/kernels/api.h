@@ -204,9 +204,17 @@ struct TcGemmArgs {
   int atomic;                   // accumulate into y (residual / split-K)
   int y_zeroed;                 // caller zeroed y (allows split-K with a plain result)
   int k_splits;
-  int bn;                       // token tile: 32, 64 or 128
+  int bn;                       // token tile: 32, 64, 128 or 256
   int* status;                  // device status word (bounded-wait errors)
   bool pdl;
+  // SwiGLU epilogue: W is a fused [gate (F rows) | up (F rows)] matrix (N = 2F); each CTA
+  // dequantises 64 gate rows and the 64 matching up rows, and writes h = silu(g) * u as bf16
+  // [M, h_stride] (no fp32 output, y unused)
+  __nv_bfloat16* h;
+  int64_t h_stride;
+  // persistent launch (one CTA per SM looping over tiles, epilogue overlapped with the next
+  // tile's main loop); no split-K
+  int persistent;
 };
 int tc_gemm_splits(int N, int M, int K, int bn, int sms);
 void tc_gemm_launch(const TcGemmArgs& g, cudaStream_t s);

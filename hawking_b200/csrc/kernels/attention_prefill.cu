@@ -1,5 +1,7 @@
 // Paged causal prefill attention on the tensor cores (K5 prefill): flash-style, one CTA per
-// (64-query-row tile, query head), bf16 mma.sync m16n8k16 with fp32 accumulation.
+// (64-query-row tile, HPC query heads of one KV group), bf16 mma.sync m16n8k16 with fp32
+// accumulation. The HPC heads (4 warps each) share every K/V tile the CTA stages, so grouped-
+// query attention moves each key and value through shared memory once per group, not per head.
 //
 // Rows are the forward's rows (row_seq picks the sequence's block-table row, row_ctx the number
 // of keys the row sees, so causality is per row and a tile may hold the tail of one sequence and
@@ -60,37 +62,39 @@ __device__ __forceinline__ uint32_t swz(int row, int c) {
   return (uint32_t)(row * HD * 2 + ((c ^ (row & 7)) << 4));
 }
 
-template <int HD>
-__global__ void __launch_bounds__(128) attn_prefill_kernel(AttnDecodeArgs a) {
+template <int HD, int HPC>
+__global__ void __launch_bounds__(128 * HPC) attn_prefill_kernel(AttnDecodeArgs a) {
   constexpr int CH = HD / 8;           // 16-byte chunks per row
   constexpr int TILE = kPfBN * HD * 2;  // bytes of one K or V tile
+  constexpr int NT = 128 * HPC;         // threads
   constexpr float kLog2e = 1.4426950408889634f;
   constexpr float NEG = -INFINITY;
   extern __shared__ __align__(128) uint8_t smem[];
-  uint8_t* qs = smem;                    // [64][HD]
-  uint8_t* ks = smem + kPfBM * HD * 2;   // [2][64][HD]
-  uint8_t* vs = ks + 2 * TILE;           // [2][64][HD]
+  uint8_t* qs_all = smem;                      // [HPC][64][HD]
+  uint8_t* ks = smem + HPC * kPfBM * HD * 2;   // [2][64][HD]
+  uint8_t* vs = ks + 2 * TILE;                 // [2][64][HD]
   __shared__ int seq_s[kPfBM], ctx_s[kPfBM];
 
   pdl_wait();
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tid = threadIdx.x, lane = tid & 31, warp = (tid >> 5) & 3, hl = tid >> 7;
   const int ntiles = (a.R + kPfBM - 1) / kPfBM;
   const int tile = ntiles - 1 - (int)blockIdx.x;  // longest rows first
-  const int h = blockIdx.y, g = h / (a.nh / a.nkv);
+  const int h = blockIdx.y * HPC + hl, g = (blockIdx.y * HPC) / (a.nh / a.nkv);
+  uint8_t* qs = qs_all + hl * kPfBM * HD * 2;  // this warp's head
   const int r0 = tile * kPfBM, nvalid = min(a.R - r0, kPfBM);
   if (tid < kPfBM) {
     seq_s[tid] = tid < nvalid ? a.row_seq[r0 + tid] : -1;
     ctx_s[tid] = tid < nvalid ? a.row_ctx[r0 + tid] : 0;
   }
-  for (int i = tid; i < kPfBM * CH; i += 128) {  // q (fp32, roped) -> bf16 tile
-    const int row = i / CH, c = i % CH;
+  for (int i = tid; i < HPC * kPfBM * CH; i += NT) {  // q (fp32, roped) -> bf16 tiles, one per head
+    const int hh = i / (kPfBM * CH), row = (i / CH) % kPfBM, c = i % CH;
     uint4 v = make_uint4(0u, 0u, 0u, 0u);
     if (row < nvalid) {
-      const float* src = a.q + ((int64_t)(r0 + row) * a.nh + h) * HD + c * 8;
+      const float* src = a.q + ((int64_t)(r0 + row) * a.nh + blockIdx.y * HPC + hh) * HD + c * 8;
       const float4 f0 = *reinterpret_cast<const float4*>(src), f1 = *reinterpret_cast<const float4*>(src + 4);
       v = make_uint4(pack_bf16(f0.x, f0.y), pack_bf16(f0.z, f0.w), pack_bf16(f1.x, f1.y), pack_bf16(f1.z, f1.w));
     }
-    *reinterpret_cast<uint4*>(qs + swz<HD>(row, c)) = v;
+    *reinterpret_cast<uint4*>(qs_all + hh * kPfBM * HD * 2 + swz<HD>(row, c)) = v;
   }
   __syncthreads();
   uint32_t qf[HD / 16][4];
@@ -123,7 +127,7 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(AttnDecodeArgs a) {
     const int nkt = (kv_len + kPfBN - 1) / kPfBN;
 
     auto load_kv = [&](int kt, int buf) {
-      for (int i = tid; i < kPfBN * CH; i += 128) {
+      for (int i = tid; i < kPfBN * CH; i += NT) {
         const int key = i / CH, c = i % CH;
         const int t = kt * kPfBN + key;
         const bool valid = t < kv_len;
@@ -303,16 +307,22 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(AttnDecodeArgs a) {
   pdl_launch();
 }
 
-template <int HD>
-void launch_prefill(const AttnDecodeArgs& a, cudaStream_t s, bool pdl) {
-  const int smem = kPfBM * HD * 2 + 4 * kPfBN * HD * 2;
+template <int HD, int HPC>
+void launch_prefill_hpc(const AttnDecodeArgs& a, cudaStream_t s, bool pdl) {
+  const int smem = HPC * kPfBM * HD * 2 + 4 * kPfBN * HD * 2;
   static bool configured = false;  // per instantiation; one device per process
   if (!configured) {
-    HK_CUDA_CHECK(cudaFuncSetAttribute(attn_prefill_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    HK_CUDA_CHECK(cudaFuncSetAttribute(attn_prefill_kernel<HD, HPC>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     configured = true;
   }
-  const dim3 grid((a.R + kPfBM - 1) / kPfBM, a.nh);
-  launch(attn_prefill_kernel<HD>, grid, dim3(128), smem, s, pdl, a);
+  const dim3 grid((a.R + kPfBM - 1) / kPfBM, a.nh / HPC);
+  launch(attn_prefill_kernel<HD, HPC>, grid, dim3(128 * HPC), smem, s, pdl, a);
+}
+
+template <int HD>
+void launch_prefill(const AttnDecodeArgs& a, cudaStream_t s, bool pdl) {
+  if ((a.nh / a.nkv) % 2 == 0) launch_prefill_hpc<HD, 2>(a, s, pdl);  // two heads of one KV group per CTA
+  else launch_prefill_hpc<HD, 1>(a, s, pdl);
 }
 
 }  // namespace

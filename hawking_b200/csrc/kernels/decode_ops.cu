@@ -87,8 +87,53 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const float* x, int64_t x_
   }
 }
 
+// Prefill-sized RMSNorm -> bf16: one CTA per row, every element loaded once as float4 into
+// registers (EPT4 vectors per thread), one block reduction, 8-byte bf16x4 stores.
+template <int EPT4>
+__global__ void __launch_bounds__(256) rmsnorm_bf16_vec_kernel(const float* x, int64_t x_stride, const float* w,
+                                                                float eps, int K, __nv_bfloat16* yb, int64_t y_stride) {
+  __shared__ float red[32];
+  pdl_wait();
+  const int r = blockIdx.x;
+  const float4* xr = reinterpret_cast<const float4*>(x + (int64_t)r * x_stride);
+  float4 v[EPT4];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < EPT4; ++j) {
+    v[j] = xr[threadIdx.x + j * 256];
+    ss += v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
+  }
+  ss = block_sum(ss, red);
+  const float scale = rsqrtf(ss / K + eps);
+  pdl_launch();
+#pragma unroll
+  for (int j = 0; j < EPT4; ++j) {
+    const int i4 = threadIdx.x + j * 256;
+    float4 wv = make_float4(1.f, 1.f, 1.f, 1.f);
+    if (w) wv = reinterpret_cast<const float4*>(w)[i4];
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(v[j].x * scale * wv.x, v[j].y * scale * wv.y);
+    const __nv_bfloat162 hi = __floats2bfloat162_rn(v[j].z * scale * wv.z, v[j].w * scale * wv.w);
+    uint2 pk;
+    pk.x = *reinterpret_cast<const uint32_t*>(&lo);
+    pk.y = *reinterpret_cast<const uint32_t*>(&hi);
+    *reinterpret_cast<uint2*>(yb + (int64_t)r * y_stride + 4 * i4) = pk;
+  }
+}
+
 void rmsnorm_launch(const float* x, int64_t x_stride, const float* w, float eps, int rows, int K, float* y_f32,
                     __nv_bfloat16* y_bf16, int64_t y_stride, cudaStream_t s, bool pdl) {
+  const bool vec = !y_f32 && y_bf16 && K % 1024 == 0 && K <= 8192 && x_stride % 4 == 0 && y_stride % 4 == 0 &&
+                   reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(y_bf16) % 8 == 0 &&
+                   reinterpret_cast<uintptr_t>(w) % 16 == 0;
+  if (vec) {
+    switch (K / 1024) {
+      case 1: launch(rmsnorm_bf16_vec_kernel<1>, dim3(rows), dim3(256), 0, s, pdl, x, x_stride, w, eps, K, y_bf16, y_stride); return;
+      case 2: launch(rmsnorm_bf16_vec_kernel<2>, dim3(rows), dim3(256), 0, s, pdl, x, x_stride, w, eps, K, y_bf16, y_stride); return;
+      case 4: launch(rmsnorm_bf16_vec_kernel<4>, dim3(rows), dim3(256), 0, s, pdl, x, x_stride, w, eps, K, y_bf16, y_stride); return;
+      case 8: launch(rmsnorm_bf16_vec_kernel<8>, dim3(rows), dim3(256), 0, s, pdl, x, x_stride, w, eps, K, y_bf16, y_stride); return;
+      default: break;
+    }
+  }
   launch(rmsnorm_kernel, dim3(rows), dim3(256), 0, s, pdl, x, x_stride, w, eps, K, y_f32, y_bf16, y_stride);
 }
 

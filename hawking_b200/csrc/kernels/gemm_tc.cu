@@ -13,6 +13,12 @@
 //               the epilogue (tcgen05.ld 32x32b -> coalesced fp32 stores or atomics)
 // Pipelines: raw (depth 4, TMA -> dequant warps) and A/X (depth 2, dequant warps + TMA -> UMMA,
 // released by tcgen05.commit). All waits are bounded and report through the status word.
+//
+// SwiGLU variant (SW): the weight is the fused [gate | up] matrix of an FFN; tile i's 128 rows are
+// gate rows [64 i, 64 i + 64) and the matching up rows [F + 64 i, ...) (two 64-row TMA boxes per
+// plane), so one TMEM accumulator holds both halves of 64 FFN columns. The epilogue warps holding
+// the up half park it in the (now idle) A stage buffers, and the gate half's warps write
+// h = silu(g) * u as bf16: the fp32 gate/up activations never reach global memory.
 // No TMA multicast is used (the kernel may run in multi-GPU processes).
 //
 // Numerics: the sub-block scale and min products are rounded to bf16 before the dequant FMA and
@@ -68,6 +74,9 @@ struct TcArgs {
   int atomic;
   int serialize;
   int* status;
+  __nv_bfloat16* h;   // SwiGLU output
+  int64_t h_stride;
+  int F;              // SwiGLU: FFN width (up rows start at F)
 };
 
 __device__ __forceinline__ uint32_t bf2_bits(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t*>(&v); }
@@ -88,7 +97,7 @@ __device__ __forceinline__ uint2 dq4(uint32_t v, int hi, __nv_bfloat162 s2, __nv
   return r;
 }
 
-template <int BN>
+template <int BN, bool SW>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_q4k_kernel(const __grid_constant__ CUtensorMap tm_hdr, const __grid_constant__ CUtensorMap tm_qs,
                        const __grid_constant__ CUtensorMap tm_x, TcArgs a) {
@@ -104,7 +113,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::n_bars);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * BM, m0 = blockIdx.y * BN;
+  // SW: n0 is the tile's first gate row (64 per tile); otherwise its first weight row
+  const int n0 = SW ? blockIdx.x * (BM / 2) : blockIdx.x * BM, m0 = blockIdx.y * BN;
   const int s0 = blockIdx.z * a.stages_per_split;
   const int s1 = min(a.stages_total, s0 + a.stages_per_split);
   const int nst = max(0, s1 - s0);
@@ -134,8 +144,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(&raw_empty[slot], ((i / L::DR) & 1) ^ 1, a.status)) break;
         const int gs = s0 + i, sb = gs >> 1, h = gs & 1;
         mbar_arrive_expect_tx(&raw_full[slot], RAW_HDR + RAW_QS);
-        tma_load_2d(smem + L::off_hdr + slot * RAW_HDR, &tm_hdr, sb * 16, n0, &raw_full[slot]);
-        tma_load_2d(smem + L::off_qs + slot * RAW_QS, &tm_qs, (2 * sb + h) * 64, n0, &raw_full[slot]);
+        if constexpr (SW) {  // 64 gate rows, then the 64 matching up rows (boxes of 64 rows)
+          tma_load_2d(smem + L::off_hdr + slot * RAW_HDR, &tm_hdr, sb * 16, n0, &raw_full[slot]);
+          tma_load_2d(smem + L::off_hdr + slot * RAW_HDR + RAW_HDR / 2, &tm_hdr, sb * 16, a.F + n0, &raw_full[slot]);
+          tma_load_2d(smem + L::off_qs + slot * RAW_QS, &tm_qs, (2 * sb + h) * 64, n0, &raw_full[slot]);
+          tma_load_2d(smem + L::off_qs + slot * RAW_QS + RAW_QS / 2, &tm_qs, (2 * sb + h) * 64, a.F + n0,
+                      &raw_full[slot]);
+        } else {
+          tma_load_2d(smem + L::off_hdr + slot * RAW_HDR, &tm_hdr, sb * 16, n0, &raw_full[slot]);
+          tma_load_2d(smem + L::off_qs + slot * RAW_QS, &tm_qs, (2 * sb + h) * 64, n0, &raw_full[slot]);
+        }
         ++issued;
       }
       // Drain: every issued copy has landed before the CTA may exit.
@@ -221,7 +239,43 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 
     // ---- epilogue: warps 4..7 (TMEM lane quarter = warp % 4) ----
-    if (warp >= kDequantWarp0 && warp < kDequantWarp0 + 4) {
+    if (SW && warp >= kDequantWarp0 && warp < kDequantWarp0 + 4) {
+      // lanes 0-63 hold gate rows, 64-127 the matching up rows: warps 6-7 park the up half in
+      // the idle A stages ([64 rows][BN] fp32 = BN * 256 bytes <= 64 KB), warps 4-5 combine
+      const bool ok = __shfl_sync(0xffffffffu, mbar_wait(acc_full, 0, a.status), 0);
+      tc_fence_after();
+      const int q = warp & 3;
+      float* park = reinterpret_cast<float*>(smem + L::off_a);  // [BN / 8][64 rows][8]
+      if (ok && q >= 2) {
+#pragma unroll 1
+        for (int j = 0; j < BN / 8; ++j) {
+          float v[8];
+          tmem_ld_x8(tmem + ((uint32_t)(q * 32) << 16) + j * 8, v);
+          tmem_wait_ld();
+          float4* dst = reinterpret_cast<float4*>(park + ((j * 64) + (q - 2) * 32 + lane) * 8);
+          dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+          dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+        }
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps
+      if (ok && q < 2) {
+        const int f = n0 + q * 32 + lane;
+#pragma unroll 1
+        for (int j = 0; j < BN / 8; ++j) {
+          float v[8];
+          tmem_ld_x8(tmem + ((uint32_t)(q * 32) << 16) + j * 8, v);
+          tmem_wait_ld();
+          const float4* src = reinterpret_cast<const float4*>(park + ((j * 64) + q * 32 + lane) * 8);
+          const float4 u0 = src[0], u1 = src[1];
+          const float u[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const int m = m0 + j * 8 + e;
+            if (m < a.M) a.h[(int64_t)m * a.h_stride + f] = __float2bfloat16(v[e] / (1.f + __expf(-v[e])) * u[e]);
+          }
+        }
+      }
+    } else if (!SW && warp >= kDequantWarp0 && warp < kDequantWarp0 + 4) {
       const bool ok = __shfl_sync(0xffffffffu, mbar_wait(acc_full, 0, a.status), 0);
       tc_fence_after();
       if (ok) {
@@ -243,6 +297,250 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  pdl_launch();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, tmem_cols);
+    tmem_relinquish();
+  }
+}
+
+// ---- persistent variant (prefill-sized M, no split-K) ------------------------------------------
+// One CTA per SM walks the tiles t = blockIdx.x, + gridDim.x, ... (weight tile major, token tile
+// minor, so the CTAs in flight share weight tiles in L2). Every role runs its own loop over the
+// same tile sequence with stage counters that continue across tiles, and the accumulator is
+// double-buffered in TMEM (2 x BN columns): the four dedicated epilogue warps drain tile j while
+// the issuer and the dequantisers already fill tile j + 1, so neither the epilogue nor a partial
+// last wave stalls the tensor cores. Stages are those of the one-tile kernel (K = 128: half a
+// Q4_K super-block, two 128-byte swizzle atoms of A and of X); 64-wide stages with twice the
+// depth measured slower (the per-stage hand-offs dominate).
+//   warp 0 raw Q4_K TMA producer, warp 1 activation TMA producer, warp 2 TMEM owner + UMMA issuer,
+//   warps 4-11 dequantisers, warps 12-15 epilogue (TMEM lane quarter = warp % 4).
+constexpr int kPThreads = 512;
+constexpr int kPEpi0 = 12;
+
+template <int BN>
+struct PLayout {
+  using L = Layout<BN>;
+  static constexpr uint32_t off_park = L::off_bar;                  // SwiGLU exchange [2][64][8] fp32
+  static constexpr uint32_t off_bar = off_park + 2 * 64 * 8 * 4;
+  static constexpr uint32_t n_bars = 2 * L::DR + 2 * DA + 4;
+  static constexpr uint32_t total = off_bar + n_bars * 8 + 16 + 1024;
+  static_assert(total <= 232448, "tc_gemm persistent: shared memory over the 227 KB per-CTA limit");
+};
+
+template <int BN, bool SW>
+__global__ void __launch_bounds__(kPThreads, 1)
+    tc_gemm_q4k_persistent(const __grid_constant__ CUtensorMap tm_hdr, const __grid_constant__ CUtensorMap tm_qs,
+                           const __grid_constant__ CUtensorMap tm_x, TcArgs a) {
+  using L = Layout<BN>;
+  using P = PLayout<BN>;
+  constexpr int PDR = L::DR, PDA = DA;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P::off_bar);
+  uint64_t* raw_full = bars;
+  uint64_t* raw_empty = bars + PDR;
+  uint64_t* a_full = bars + 2 * PDR;
+  uint64_t* a_empty = bars + 2 * PDR + PDA;
+  uint64_t* acc_full = bars + 2 * PDR + 2 * PDA;   // [2]
+  uint64_t* acc_empty = acc_full + 2;              // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + P::n_bars);
+  float* park = reinterpret_cast<float*>(smem + P::off_park);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int RB = SW ? BM / 2 : BM;  // weight rows (gate rows under SW) a tile advances by
+  const int m_tiles = (a.M + BN - 1) / BN;
+  const int n_tiles = SW ? a.F / RB : a.N / BM;
+  const int tiles = m_tiles * n_tiles;
+  const int nst = a.K / BK;
+  constexpr uint32_t tmem_cols = 2 * BN;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < PDR; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], kDequantWarps); }
+    for (int i = 0; i < PDA; ++i) { mbar_init(&a_full[i], kDequantWarps + 1); mbar_init(&a_empty[i], 1); }
+    for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 4); }
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) { prefetch_tmap(&tm_hdr); prefetch_tmap(&tm_qs); prefetch_tmap(&tm_x); }
+  if (warp == 2) tmem_alloc(tmem_slot, tmem_cols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (warp != 0) pdl_wait();  // weights do not depend on the previous kernel
+
+  if (warp == 0 && lane == 0) {
+    // ---- raw Q4_K producer: stage s = half (s & 1) of super-block (s >> 1) ----
+    int it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+      const int n0 = (t / m_tiles) * RB;
+      for (int s = 0; s < nst; ++s, ++it) {
+        const int slot = it % PDR;
+        if (!(ok = mbar_wait(&raw_empty[slot], ((it / PDR) & 1) ^ 1, a.status))) break;
+        const int sb = s >> 1, h = s & 1;
+        mbar_arrive_expect_tx(&raw_full[slot], RAW_HDR + RAW_QS);
+        uint8_t* hd = smem + L::off_hdr + slot * RAW_HDR;
+        uint8_t* qd = smem + L::off_qs + slot * RAW_QS;
+        if constexpr (SW) {
+          tma_load_2d(hd, &tm_hdr, sb * 16, n0, &raw_full[slot]);
+          tma_load_2d(hd + RAW_HDR / 2, &tm_hdr, sb * 16, a.F + n0, &raw_full[slot]);
+          tma_load_2d(qd, &tm_qs, (2 * sb + h) * 64, n0, &raw_full[slot]);
+          tma_load_2d(qd + RAW_QS / 2, &tm_qs, (2 * sb + h) * 64, a.F + n0, &raw_full[slot]);
+        } else {
+          tma_load_2d(hd, &tm_hdr, sb * 16, n0, &raw_full[slot]);
+          tma_load_2d(qd, &tm_qs, (2 * sb + h) * 64, n0, &raw_full[slot]);
+        }
+      }
+    }
+    // drain: every issued copy has landed before the CTA may exit
+    for (int i = max(0, it - PDR); i < it; ++i) mbar_wait(&raw_full[i % PDR], (i / PDR) & 1, nullptr, 1u << 22);
+  } else if (warp == 1 && lane == 0) {
+    // ---- activation producer ----
+    int it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+      const int m0 = (t % m_tiles) * BN;
+      for (int s = 0; s < nst; ++s, ++it) {
+        const int slot = it % PDA;
+        if (!(ok = mbar_wait(&a_empty[slot], ((it / PDA) & 1) ^ 1, a.status))) break;
+        mbar_arrive_expect_tx(&a_full[slot], L::X_STAGE);
+        uint8_t* xs = smem + L::off_x + slot * L::X_STAGE;
+        tma_load_2d(xs, &tm_x, s * BK, m0, &a_full[slot]);
+        tma_load_2d(xs + L::X_ATOM, &tm_x, s * BK + 64, m0, &a_full[slot]);
+      }
+    }
+    if (!ok) for (int k = 0; k < 2000; ++k) __nanosleep(100);  // error path: let copies in flight land
+  } else if (warp == 2 && lane == 0) {
+    // ---- UMMA issuer ----
+    constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
+    int it = 0, j = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++j) {
+      const int ab = j & 1;
+      if (!(ok = mbar_wait(&acc_empty[ab], ((j >> 1) & 1) ^ 1, a.status))) break;
+      tc_fence_after();
+      const uint32_t acc = tmem + (uint32_t)(ab * BN);
+      for (int s = 0; s < nst; ++s, ++it) {
+        const int slot = it % PDA;
+        if (!(ok = mbar_wait(&a_full[slot], (it / PDA) & 1, a.status))) break;
+        tc_fence_after();
+        const uint32_t a_base = smem_u32(smem + L::off_a + slot * A_STAGE);
+        const uint32_t x_base = smem_u32(smem + L::off_x + slot * L::X_STAGE);
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_f16(acc, sdesc_k_sw128(a_base + c * A_ATOM + kk * 32), sdesc_k_sw128(x_base + c * L::X_ATOM + kk * 32),
+                     idesc, (s | c | kk) != 0);
+        umma_commit(&a_empty[slot]);
+      }
+      if (ok) umma_commit(&acc_full[ab]);
+    }
+  } else if (warp >= kDequantWarp0 && warp < kDequantWarp0 + kDequantWarps) {
+    // ---- dequantisers: thread (row r, chunk c) expands the 32 quant bytes of chunk c of the
+    // stage's half super-block (low nibbles: sub-block 4h + 2c, high: 4h + 2c + 1)
+    const int tt = (warp - kDequantWarp0) * 32 + lane;
+    const int r = tt >> 1, c = tt & 1;
+    int it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+      for (int s = 0; s < nst; ++s, ++it) {
+        const int rs = it % PDR, as = it % PDA;
+        ok = __shfl_sync(0xffffffffu, mbar_wait(&raw_full[rs], (it / PDR) & 1, a.status), 0);
+        if (!ok) break;
+        const uint4 hdr = *reinterpret_cast<const uint4*>(smem + L::off_hdr + rs * RAW_HDR + r * 16);
+        const uint4 q0 = *reinterpret_cast<const uint4*>(smem + L::off_qs + rs * RAW_QS + r * 64 + c * 32);
+        const uint4 q1 = *reinterpret_cast<const uint4*>(smem + L::off_qs + rs * RAW_QS + r * 64 + c * 32 + 16);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&raw_empty[rs]);  // raw values are in registers now
+        const int j0 = 4 * (s & 1) + 2 * c;
+        int sc0, mn0, sc1, mn1;
+        q4k_scale_min(j0, hdr.y, hdr.z, hdr.w, sc0, mn0);
+        q4k_scale_min(j0 + 1, hdr.y, hdr.z, hdr.w, sc1, mn1);
+        const float d = __half2float(__ushort_as_half((uint16_t)(hdr.x & 0xFFFF)));
+        const float dm = __half2float(__ushort_as_half((uint16_t)(hdr.x >> 16)));
+        const __nv_bfloat162 s2A = __float2bfloat162_rn(d * sc0), s2B = __float2bfloat162_rn(d * sc1);
+        const __nv_bfloat162 o2A = __float2bfloat162_rn(-dm * mn0), o2B = __float2bfloat162_rn(-dm * mn1);
+        ok = __shfl_sync(0xffffffffu, mbar_wait(&a_empty[as], ((it / PDA) & 1) ^ 1, a.status), 0);
+        if (!ok) break;
+        uint8_t* atom = smem + L::off_a + as * A_STAGE + c * A_ATOM;
+        const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) {  // 16-byte chunk = 8 elements = 2 words
+          const uint2 lo0 = dq4(w[2 * ch], 0, s2A, o2A), lo1 = dq4(w[2 * ch + 1], 0, s2A, o2A);
+          const uint2 hi0 = dq4(w[2 * ch], 1, s2B, o2B), hi1 = dq4(w[2 * ch + 1], 1, s2B, o2B);
+          *reinterpret_cast<uint4*>(atom + sw128_offset(r, ch)) = make_uint4(lo0.x, lo0.y, lo1.x, lo1.y);
+          *reinterpret_cast<uint4*>(atom + sw128_offset(r, ch + 4)) = make_uint4(hi0.x, hi0.y, hi1.x, hi1.y);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&a_full[as]);
+      }
+    }
+  } else if (warp >= kPEpi0) {
+    // ---- epilogue ----
+    const int q = warp & 3;
+    int j = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++j) {
+      const int ab = j & 1;
+      const bool ok = __shfl_sync(0xffffffffu, mbar_wait(&acc_full[ab], (j >> 1) & 1, a.status), 0);
+      if (!ok) break;
+      tc_fence_after();
+      const int n0 = (t / m_tiles) * RB, m0 = (t % m_tiles) * BN;
+      const uint32_t acc = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BN);
+      if constexpr (SW) {
+        // lanes 0-63: gate rows n0.., lanes 64-127: the matching up rows; warps q = 2, 3 hand their
+        // up values to warps q = 0, 1 through a two-slot park, 8 tokens at a time
+        const int f = n0 + (q & 1) * 32 + lane;
+#pragma unroll 1
+        for (int cj = 0; cj < BN / 8; ++cj) {
+          float v[8];
+          tmem_ld_x8(acc + cj * 8, v);
+          tmem_wait_ld();
+          float* slot = park + ((cj & 1) * 64 + (q & 1) * 32 + lane) * 8;
+          if (q >= 2) {
+            reinterpret_cast<float4*>(slot)[0] = make_float4(v[0], v[1], v[2], v[3]);
+            reinterpret_cast<float4*>(slot)[1] = make_float4(v[4], v[5], v[6], v[7]);
+          }
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          if (q < 2) {
+            const float4 u0 = reinterpret_cast<const float4*>(slot)[0], u1 = reinterpret_cast<const float4*>(slot)[1];
+            const float u[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const int m = m0 + cj * 8 + e;
+              if (m < a.M) a.h[(int64_t)m * a.h_stride + f] = __float2bfloat16(v[e] / (1.f + __expf(-v[e])) * u[e]);
+            }
+          }
+          // slot cj & 1 is rewritten at cj + 2, after the next chunk's barrier: no second barrier
+        }
+      } else {
+        const int n = n0 + q * 32 + lane;
+#pragma unroll 1
+        for (int cj = 0; cj < BN / 8; ++cj) {
+          float v[8];
+          tmem_ld_x8(acc + cj * 8, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const int m = m0 + cj * 8 + e;
+            if (m < a.M && n < a.N) {
+              float* dst = a.y + (int64_t)m * a.y_stride + n;
+              if (a.atomic) atomicAdd(dst, v[e]);
+              else *dst = v[e];
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[ab]);
     }
   }
   tc_fence_before();
@@ -284,12 +582,14 @@ CUtensorMap make_map_2d(CUtensorMapDataType dt, const void* base, uint64_t inner
   return m;
 }
 
-template <int BN>
+template <int BN, bool SW>
 void launch_bn(const TcGemmArgs& g, cudaStream_t s) {
   using L = Layout<BN>;
   const uint64_t rb = (uint64_t)g.w_row_bytes, hb = (uint64_t)g.w_hdr_row_bytes;
-  CUtensorMap tm_hdr = make_map_2d(CU_TENSOR_MAP_DATA_TYPE_UINT8, g.w_hdr, hb, g.N, hb, 16, BM, CU_TENSOR_MAP_SWIZZLE_NONE);
-  CUtensorMap tm_qs = make_map_2d(CU_TENSOR_MAP_DATA_TYPE_UINT8, g.w, rb, g.N, rb, 64, BM, CU_TENSOR_MAP_SWIZZLE_NONE);
+  const uint32_t box_rows = SW ? BM / 2 : BM;
+  CUtensorMap tm_hdr = make_map_2d(CU_TENSOR_MAP_DATA_TYPE_UINT8, g.w_hdr, hb, g.N, hb, 16, box_rows,
+                                   CU_TENSOR_MAP_SWIZZLE_NONE);
+  CUtensorMap tm_qs = make_map_2d(CU_TENSOR_MAP_DATA_TYPE_UINT8, g.w, rb, g.N, rb, 64, box_rows, CU_TENSOR_MAP_SWIZZLE_NONE);
   CUtensorMap tm_x = make_map_2d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, g.x, g.K, g.M, (uint64_t)g.x_stride * 2, 64, BN,
                                  CU_TENSOR_MAP_SWIZZLE_128B);
   TcArgs a;
@@ -305,13 +605,55 @@ void launch_bn(const TcGemmArgs& g, cudaStream_t s) {
   a.atomic = (g.atomic || splits > 1) ? 1 : 0;
   a.status = g.status;
   a.serialize = getenv("HK_GEMM_SERIALIZE") != nullptr;
+  a.h = g.h;
+  a.h_stride = g.h_stride;
+  a.F = g.N / 2;
+  if (SW && splits != 1) throw std::runtime_error("tc_gemm swiglu: no split-K");
   static bool attr_set = false;
   if (!attr_set) {
-    HK_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_q4k_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::total));
+    HK_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_q4k_kernel<BN, SW>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::total));
     attr_set = true;
   }
   dim3 grid(g.N / BM, (g.M + BN - 1) / BN, splits);
-  launch(tc_gemm_q4k_kernel<BN>, grid, dim3(kThreads), L::total, s, g.pdl, tm_hdr, tm_qs, tm_x, a);
+  launch(tc_gemm_q4k_kernel<BN, SW>, grid, dim3(kThreads), L::total, s, g.pdl, tm_hdr, tm_qs, tm_x, a);
+}
+
+template <int BN, bool SW>
+void launch_persistent(const TcGemmArgs& g, cudaStream_t s) {
+  using P = PLayout<BN>;
+  const uint64_t rb = (uint64_t)g.w_row_bytes, hb = (uint64_t)g.w_hdr_row_bytes;
+  const uint32_t box_rows = SW ? BM / 2 : BM;
+  CUtensorMap tm_hdr = make_map_2d(CU_TENSOR_MAP_DATA_TYPE_UINT8, g.w_hdr, hb, g.N, hb, 16, box_rows,
+                                   CU_TENSOR_MAP_SWIZZLE_NONE);
+  CUtensorMap tm_qs = make_map_2d(CU_TENSOR_MAP_DATA_TYPE_UINT8, g.w, rb, g.N, rb, 64, box_rows, CU_TENSOR_MAP_SWIZZLE_NONE);
+  CUtensorMap tm_x = make_map_2d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, g.x, g.K, g.M, (uint64_t)g.x_stride * 2, 64, BN,
+                                 CU_TENSOR_MAP_SWIZZLE_128B);
+  TcArgs a{};
+  a.N = g.N;
+  a.K = g.K;
+  a.M = g.M;
+  a.stages_total = g.K / BK;
+  a.stages_per_split = a.stages_total;
+  a.y = g.y;
+  a.y_stride = g.y_stride;
+  a.atomic = g.atomic ? 1 : 0;
+  a.status = g.status;
+  a.h = g.h;
+  a.h_stride = g.h_stride;
+  a.F = g.N / 2;
+  static bool attr_set = false;
+  static int sms = 0;
+  if (!attr_set) {
+    HK_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_q4k_persistent<BN, SW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       P::total));
+    int dev = 0;
+    HK_CUDA_CHECK(cudaGetDevice(&dev));
+    HK_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    attr_set = true;
+  }
+  const int tiles = ((g.M + BN - 1) / BN) * (g.N / BM);
+  launch(tc_gemm_q4k_persistent<BN, SW>, dim3(std::min(tiles, sms)), dim3(kPThreads), P::total, s, g.pdl, tm_hdr,
+         tm_qs, tm_x, a);
 }
 
 }  // namespace
@@ -329,11 +671,33 @@ void tc_gemm_launch(const TcGemmArgs& g, cudaStream_t s) {
   if (g.N % BM) throw std::runtime_error("tc_gemm: N must be a multiple of 128");
   if (g.K % 256) throw std::runtime_error("tc_gemm: K must be a multiple of 256");
   if (g.k_splits > 1 && !g.atomic && !g.y_zeroed) throw std::runtime_error("tc_gemm: split-K needs a zeroed output");
+  if (g.persistent) {  // prefill-sized M: persistent CTAs, double-buffered TMEM accumulators
+    if (g.bn != 256 && g.bn != 128) throw std::runtime_error("tc_gemm persistent: bn must be 128 or 256");
+    if (g.h && g.N % 128) throw std::runtime_error("tc_gemm swiglu: F must be a multiple of 64");
+    if (g.h) {
+      if (g.bn == 256) launch_persistent<256, true>(g, s);
+      else launch_persistent<128, true>(g, s);
+    } else {
+      if (g.bn == 256) launch_persistent<256, false>(g, s);
+      else launch_persistent<128, false>(g, s);
+    }
+    return;
+  }
+  if (g.h) {  // fused SwiGLU epilogue
+    if (g.N % 128) throw std::runtime_error("tc_gemm swiglu: F must be a multiple of 64");
+    switch (g.bn) {
+      case 64: launch_bn<64, true>(g, s); break;
+      case 128: launch_bn<128, true>(g, s); break;
+      case 256: launch_bn<256, true>(g, s); break;
+      default: throw std::runtime_error("tc_gemm swiglu: bn must be 64, 128 or 256");
+    }
+    return;
+  }
   switch (g.bn) {
-    case 32: launch_bn<32>(g, s); break;
-    case 64: launch_bn<64>(g, s); break;
-    case 128: launch_bn<128>(g, s); break;
-    case 256: launch_bn<256>(g, s); break;
+    case 32: launch_bn<32, false>(g, s); break;
+    case 64: launch_bn<64, false>(g, s); break;
+    case 128: launch_bn<128, false>(g, s); break;
+    case 256: launch_bn<256, false>(g, s); break;
     default: throw std::runtime_error("tc_gemm: bn must be 32, 64, 128 or 256");
   }
 }

@@ -230,6 +230,9 @@ class LlamaModel:
         # set by the caller when the forward's rows hold long runs of one sequence (prefill chunks):
         # attention then runs on the tensor-core prefill kernel instead of the split-KV decode kernel
         self.long_runs = False
+        # SwiGLU in the tensor-core GEMM epilogue (the persistent GEMM overlaps that epilogue with
+        # the next tile's main loop; the fp32 gate/up activations never reach global memory)
+        self.fuse_swiglu_tc = True
         if tp is not None:
             self.x2 = torch.zeros(R, H, device=self.dev)       # second residual buffer (push all-reduce)
             self.partial = torch.zeros(R, H, device=self.dev)  # prefill partial sums (NCCL all-reduce)
@@ -462,9 +465,14 @@ class LlamaModel:
         x = self.x[:rows]
         F = lw.w_down.K
         ops.rmsnorm(x, lw.ffn_norm, self.cfg.eps, yb=self.xb[:rows])
-        gu = self.gu[:rows, : 2 * F]
-        ops.tc_gemm(lw.w_gu, self.xb[:rows], gu, self.status, y_zeroed=True)
-        ops.swiglu_bf16(gu, F, self.hb[:rows, :F], clear=True)
+        bn = 64 if rows <= 64 else (128 if rows < 192 else 256)
+        if self.fuse_swiglu_tc and F % 64 == 0 and lw.w_gu.N == 2 * F and (F // 64) * -(-rows // bn) >= 148:
+            # SwiGLU in the GEMM epilogue (enough tiles to fill the GPU without split-K)
+            ops.tc_gemm_swiglu(lw.w_gu, self.xb[:rows], self.hb[:rows, :F], self.status, bn=bn)
+        else:
+            gu = self.gu[:rows, : 2 * F]
+            ops.tc_gemm(lw.w_gu, self.xb[:rows], gu, self.status, y_zeroed=True)
+            ops.swiglu_bf16(gu, F, self.hb[:rows, :F], clear=True)
         if self.tp is not None:
             self.partial[:rows].zero_()
             ops.tc_gemm(lw.w_down, self.hb[:rows, :F], self.partial[:rows], self.status, atomic=True, y_zeroed=True)

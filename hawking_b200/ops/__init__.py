@@ -197,6 +197,11 @@ def embed(table: QWeight, ids: torch.Tensor, out: torch.Tensor):
     kernels().embed(table.fmt, table.planes, ids, out, PDL)
 
 
+# Prefill-sized tensor-core GEMMs (256-token tiles) run as persistent kernels (one CTA per SM,
+# epilogue overlapped with the next tile's main loop).
+PERSISTENT_GEMM = True
+
+
 def tc_gemm(w: QWeight, x: torch.Tensor, y: torch.Tensor, status: torch.Tensor, atomic: bool = False,
             y_zeroed: bool = False, k_splits: int = 0, bn: int = 0):
     """y[M, N] (+)= x[M, K] (bf16) @ w[N, K]^T on the tensor cores (Q4_K weights).
@@ -207,10 +212,25 @@ def tc_gemm(w: QWeight, x: torch.Tensor, y: torch.Tensor, status: torch.Tensor, 
     if bn == 0:
         # prefill-sized M: 256-token tiles halve the dequantisation per FLOP
         bn = 32 if M <= 32 else (64 if M <= 64 else (128 if M < 192 else 256))
-    if k_splits == 0 or k_splits is None:
+    persistent = bn == 256 and k_splits in (0, None, 1) and PERSISTENT_GEMM
+    if persistent:
+        k_splits = 1  # one CTA per SM walks the tiles: the grid is full without split-K
+    elif k_splits == 0 or k_splits is None:
         k_splits = kernels().tc_gemm_splits(w.N, M, w.K, bn, 148) if (atomic or y_zeroed) else 1
     launches.add()
-    kernels().tc_gemm(w.fmt, w.planes, w.N, w.K, x, y, atomic, y_zeroed, k_splits, bn, status, PDL)
+    kernels().tc_gemm(w.fmt, w.planes, w.N, w.K, x, y, atomic, y_zeroed, k_splits, bn, status, PDL,
+                      persistent=persistent)
+
+
+def tc_gemm_swiglu(w_gu: QWeight, x: torch.Tensor, h: torch.Tensor, status: torch.Tensor, bn: int = 0):
+    """h[M, F] = silu(x @ gate^T) * (x @ up^T) as bf16, from the fused [gate | up] Q4_K weight
+    (2F rows) in one tensor-core launch (the SwiGLU runs in the GEMM epilogue)."""
+    M = x.shape[0]
+    if bn == 0:
+        bn = 64 if M <= 64 else (128 if M < 192 else 256)
+    launches.add()
+    kernels().tc_gemm(w_gu.fmt, w_gu.planes, w_gu.N, w_gu.K, x, h, False, False, 1, bn, status, PDL, h=h,
+                      persistent=bn == 256 and PERSISTENT_GEMM)
 
 
 def swiglu_bf16(gu: torch.Tensor, F: int, h: torch.Tensor, clear: bool = True):

@@ -137,6 +137,14 @@ def _tc_cases(dev, ctx, rows, g, only, bn=0):
         cases[name] = (lambda i, ws=ws, y=y, k=k: ops.tc_gemm(ws[i % len(ws)], x[:, :k], y, status, atomic=True,
                                                                          bn=bn),
                        one, 2.0 * rows * n * k)
+    if "tc_gate_up_swiglu" in only:
+        from hawking_b200.ops import cat_rows
+        one = 2 * F * H * 144 // 256
+        ws = [cat_rows([QWeight.random(GgmlType.Q4_K, F, H, 0.02, g, dev), QWeight.random(GgmlType.Q4_K, F, H, 0.02, g, dev)])
+              for _ in range(max(1, -(-(256 << 20) // one)))]
+        hb = torch.zeros(rows, F, dtype=torch.bfloat16, device=dev)
+        cases["tc_gate_up_swiglu"] = (lambda i: ops.tc_gemm_swiglu(ws[i % len(ws)], x[:, :H], hb, status, bn=bn),
+                                      one, 2.0 * rows * 2 * F * H)
     if "attention_prefill" in only:
         nblk = (ctx + BS - 1) // BS
         kc = torch.randn(nblk, NKV, BS, HD, device=dev).bfloat16()

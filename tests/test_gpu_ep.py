@@ -37,7 +37,7 @@ def _worker(rank, world, port, out_path):
         from hawking_b200.parallel.ep import local_deepseek_config, shard_deepseek_weights
         from hawking_b200.parallel.tp import TPComm
         from test_gpu_deepseek import tiny_cfg
-        cfg = tiny_cfg().with_(layers=4, first_dense_layers=1, n_heads=8, n_kv_heads=8)
+        cfg = tiny_cfg().with_(layers=4, first_dense_layers=1, n_heads=8, n_kv_heads=8, hidden=512)
         w = random_deepseek_weights(cfg, dev, seed=3, std=0.05)  # same seed: identical on every rank
         tp = TPComm(rank, world, 2 * cfg.layers, 8, cfg.hidden, dev)
         kv = LatentCache(cfg.layers, 32, 16, 2, 16, dev)

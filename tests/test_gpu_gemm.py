@@ -75,3 +75,51 @@ def test_tc_gemm_large_n_covers_grid():
     torch.cuda.synchronize()
     assert st.item() == 0
     _check(y, ref)
+
+
+@pytest.mark.parametrize("M,bn", [(100, 128), (300, 256), (64, 64)])
+def test_tc_gemm_swiglu_epilogue(M, bn):
+    """Fused [gate | up] GEMM with the SwiGLU in the epilogue vs the fp32 reference."""
+    from hawking_b200.ops import cat_rows
+    F, K = 192, 512
+    g = torch.Generator(device=DEV).manual_seed(M)
+    wg = QWeight.quantize(torch.randn(F, K, device=DEV, generator=g) * 0.05, GgmlType.Q4_K)
+    wu = QWeight.quantize(torch.randn(F, K, device=DEV, generator=g) * 0.05, GgmlType.Q4_K)
+    w = cat_rows([wg, wu])
+    x = torch.randn(M, K, device=DEV, generator=g).bfloat16()
+    gt, up = x.float() @ wg.dequantize().T, x.float() @ wu.dequantize().T
+    ref = gt / (1 + torch.exp(-gt)) * up
+    h = torch.zeros(M, F, dtype=torch.bfloat16, device=DEV)
+    st = torch.zeros(1, dtype=torch.int32, device=DEV)
+    ops.tc_gemm_swiglu(w, x, h, st, bn=bn)
+    torch.cuda.synchronize()
+    assert st.item() == 0
+    _check(h.float(), ref)
+
+
+@pytest.mark.parametrize("M,N,swiglu", [(300, 512, False), (1000, 384, False), (520, 384, True), (257, 256, True)])
+def test_tc_gemm_persistent(M, N, swiglu):
+    """Persistent tcgen05 GEMM (tiles looped per CTA, double-buffered TMEM accumulators), plain
+    store and fused SwiGLU epilogues, more tiles than CTAs and a ragged last token tile."""
+    from hawking_b200.ops import cat_rows
+    K = 512
+    g = torch.Generator(device=DEV).manual_seed(M + N)
+    st = torch.zeros(1, dtype=torch.int32, device=DEV)
+    x = torch.randn(M, K, device=DEV, generator=g).bfloat16()
+    if swiglu:
+        F = N // 2
+        wg = QWeight.quantize(torch.randn(F, K, device=DEV, generator=g) * 0.05, GgmlType.Q4_K)
+        wu = QWeight.quantize(torch.randn(F, K, device=DEV, generator=g) * 0.05, GgmlType.Q4_K)
+        gt, up = x.float() @ wg.dequantize().T, x.float() @ wu.dequantize().T
+        ref = gt / (1 + torch.exp(-gt)) * up
+        h = torch.zeros(M, F, dtype=torch.bfloat16, device=DEV)
+        ops.tc_gemm_swiglu(cat_rows([wg, wu]), x, h, st, bn=256)
+        out = h.float()
+    else:
+        w = QWeight.quantize(torch.randn(N, K, device=DEV, generator=g) * 0.02, GgmlType.Q4_K)
+        ref = x.float() @ w.dequantize().T
+        out = torch.zeros(M, N, device=DEV)
+        ops.tc_gemm(w, x, out, st, bn=256)
+    torch.cuda.synchronize()
+    assert st.item() == 0
+    _check(out, ref)

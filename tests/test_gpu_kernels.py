@@ -267,3 +267,15 @@ def test_gemv_fused_norm_matches_separate(K, nb):
     ops.gemv_swiglu(w, wu, a, h_ref)
     ops.gemv_norm_swiglu(w, wu, x, nw, 1e-5, h)
     torch.testing.assert_close(h.dequantize(), h_ref.dequantize(), rtol=1e-3, atol=2e-2 * h_ref.dequantize().abs().max().item())
+
+
+@pytest.mark.parametrize("rows,K", [(5, 4096), (3, 1024), (2, 640)])
+def test_rmsnorm_bf16_matches(rows, K):
+    """RMSNorm -> bf16 (the prefill input of the tensor-core GEMMs), vectorised and generic paths."""
+    g = torch.Generator(device="cuda").manual_seed(K)
+    x = torch.randn(rows, K, device="cuda", generator=g) * 3
+    w = torch.rand(K, device="cuda", generator=g) + 0.5
+    yb = torch.zeros(rows, K, dtype=torch.bfloat16, device="cuda")
+    ops.rmsnorm(x, w, 1e-5, yb=yb)
+    ref = x * torch.rsqrt((x * x).mean(1, keepdim=True) + 1e-5) * w
+    torch.testing.assert_close(yb.float(), ref, rtol=1e-2, atol=1e-2)
