@@ -543,7 +543,12 @@ def main():
     for s in seqs:
         kv.drop(s)
     result_bs64 = None
-    if args.bs64 and B != 64:
+    if args.bs64 and B != 64 and m.row_limit < 64:
+        # tensor parallel without the tensor-core path (MoE layers): the push all-reduce sites
+        # hold 8 rows per forward
+        result_bs64 = {"unavailable": "batch 64 under tensor/expert parallelism needs the tensor-core path, "
+                                      "which MoE layers do not have yet (forwards of <= 8 rows only)"}
+    elif args.bs64 and B != 64:
         seqs = setup_decode(64, 2_000_000)
         ms64, clocks64 = timed_decode(64)
         result_bs64 = {"tok_s_aggregate": round(64 * 1000.0 / ms64 * replicas, 1), "ms_per_step": round(ms64, 4),

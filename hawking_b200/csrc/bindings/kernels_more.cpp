@@ -183,8 +183,14 @@ void moe_gemv(int64_t fmt, int64_t epi, const std::vector<Tensor>& w0, const std
               const Tensor& xq, const Tensor& xd, const Tensor& xs, const c10::optional<Tensor>& oq,
               const c10::optional<Tensor>& od, const c10::optional<Tensor>& os, const c10::optional<Tensor>& y,
               const c10::optional<Tensor>& route_w, bool pdl, int64_t e_lo, int64_t T,
-              const c10::optional<Tensor>& push_table, const c10::optional<Tensor>& push_epoch) {
+              const c10::optional<Tensor>& push_table, const c10::optional<Tensor>& push_epoch,
+              const c10::optional<Tensor>& base) {
   hk::MoeGemvArgs a{};
+  if (base.has_value()) {
+    TORCH_CHECK(base->scalar_type() == at::kFloat && base->stride(-1) == 1, "moe_gemv: fp32 base rows");
+    a.base = base->data_ptr<float>();
+    a.base_stride = base->stride(0);
+  }
   a.e_lo = (int)e_lo;
   a.T = (int)T;
   if (push_table.has_value()) {
@@ -250,7 +256,7 @@ void register_more_kernels(py::module_& m) {
         py::arg("xq"), py::arg("xd"), py::arg("xs"), py::arg("oq") = py::none(), py::arg("od") = py::none(),
         py::arg("os") = py::none(), py::arg("y") = py::none(), py::arg("route_w") = py::none(),
         py::arg("pdl") = false, py::arg("e_lo") = 0, py::arg("T") = 0, py::arg("push_table") = py::none(),
-        py::arg("push_epoch") = py::none());
+        py::arg("push_epoch") = py::none(), py::arg("base") = py::none());
   m.def("swiglu_bf16", &swiglu_bf16, py::arg("gu"), py::arg("F"), py::arg("h"), py::arg("clear") = true,
         py::arg("pdl") = false);
 }

@@ -306,6 +306,8 @@ struct MoeGemvArgs {
   unsigned long long* const* push_recv;
   const int* push_epoch;
   int push_n;
+  const float* base;     // epi 2: optional [T, base_stride] fp32 rows added to each token's sum
+  int64_t base_stride;
 };
 void moe_gemv_launch(int fmt, int epi, const MoeGemvArgs& a, cudaStream_t s, bool pdl);
 

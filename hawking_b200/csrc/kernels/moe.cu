@@ -491,6 +491,7 @@ __global__ void __launch_bounds__(256) moe_combine_push_kernel(MoeGemvArgs a, in
   }
   pdl_launch();
   if (lane < a.T) {
+    if (a.base) acc += a.base[(int64_t)lane * a.base_stride + n];
     const uint32_t flag = (uint32_t)*a.push_epoch;
     for (int p = 0; p < a.push_n; ++p) ll_store(a.push_recv[p] + (int64_t)lane * a.N + n, __float_as_uint(acc), flag);
   }

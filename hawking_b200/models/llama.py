@@ -410,8 +410,11 @@ class LlamaModel:
         self._rope_attention(l, lw, rows, splits, out_q8=self.att.view(rows))
         ops.gemv_push(lw.wo, self._q8_slice(self.att, 0, rows), tp, 2 * l)
         ops.tp_allreduce_rmsnorm_q8(tp, 2 * l, xa_res, xb_res, lw.ffn_norm, cfg.eps, self.xa.view(rows))
-        ops.gemv_swiglu(lw.w_gate, lw.w_up, self.xa_view(0, rows), self._q8_slice(self.hq, 0, rows))
-        ops.gemv_push(lw.w_down, self._q8_slice(self.hq, 0, rows, lw.w_down.K), tp, 2 * l + 1)
+        if lw.moe is not None:  # expert parallel; the experts' combine is this site's push
+            lw.moe.forward_ep(self, rows, 2 * l + 1)
+        else:
+            ops.gemv_swiglu(lw.w_gate, lw.w_up, self.xa_view(0, rows), self._q8_slice(self.hq, 0, rows))
+            ops.gemv_push(lw.w_down, self._q8_slice(self.hq, 0, rows, lw.w_down.K), tp, 2 * l + 1)
         nxt = w.layers[l + 1].attn_norm if l + 1 < len(w.layers) else w.out_norm
         ops.tp_allreduce_rmsnorm_q8(tp, 2 * l + 1, xb_res, xa_res, nxt, cfg.eps, self.xa.view(rows))
 

@@ -19,6 +19,7 @@ from typing import Optional
 import torch
 
 from .. import ops
+from .._ext import kernels
 from ..formats.ggml import type_id
 from ..ops import Q8Act, QWeight, cat_rows
 from .config import ModelConfig
@@ -37,6 +38,8 @@ class MoEFFN:
     sh_gu: Optional[QWeight] = None
     sh_down: Optional[QWeight] = None
     sh_gate_w: Optional[torch.Tensor] = None     # fp32 [1, H] sigmoid gate of the shared expert
+    e_lo: int = 0                      # expert parallel: this rank stacks experts e_lo ..
+    n_local: int = 0                   # .. e_lo + n_local - 1 (0: all of them)
 
     @property
     def nbytes(self) -> int:
@@ -106,6 +109,91 @@ class MoEFFN:
                 glog=torch.zeros(R, 1, device=dev))
             setattr(model, key, buf)
         return buf
+
+    def forward_ep(self, model, rows: int, site: int):
+        """Expert-parallel MoE for tensor-parallel decode: the router and top-k run on every rank
+        (the normed hidden state in ``model.xa`` is replicated), this rank's experts run their
+        pairs, and the down projection's epilogue pushes each token's sum over this rank's
+        experts (plus this rank's slice of the shared expert) to every rank's receive region of
+        ``site``; the next RMSNorm adds the ranks' contributions. No token is dispatched."""
+        from .. import ops as O
+        cfg, tp = self.cfg, model.tp
+        b = self._buffers(model)
+        E, k, H, Fe = cfg.n_experts, cfg.top_k, cfg.hidden, cfg.expert_ffn
+        ne = self.n_local or E
+        xa = model.xa.view(rows)
+        O.router_logits(self.router_w, xa, b["logits"][:rows])
+        scoring = 1 if cfg.router == "sigmoid_bias" else 0
+        O.moe_topk(b["logits"][:rows], self.router_bias, k, scoring, cfg.n_groups if scoring else 1,
+                   cfg.topk_groups if scoring else 1, cfg.norm_topk, cfg.routed_scale, b["ids"][:rows],
+                   b["weights"][:rows])
+        O.moe_align(b["ids"][:rows], E, xa, b["counts"], b["offsets"], b["sorted"], b["gx"])
+        K = kernels()
+        O.launches.add(2)
+        K.moe_gemv(self.w_gate.fmt, 0, self.w_gate.planes, self.w_up.planes, Fe, self.w_gate.K, ne, k, b["counts"],
+                   b["offsets"], b["sorted"], b["gx"].q, b["gx"].d, b["gx"].s, b["h"].q, b["h"].d, b["h"].s, None, None,
+                   O.PDL, e_lo=self.e_lo)
+        base = None
+        if self.sh_down is not None:  # this rank's FFN slice of the shared expert, added by the push
+            hs_v = model._q8_slice(b["hs"], 0, rows, self.sh_gate.N)
+            O.gemv_swiglu(self.sh_gate, self.sh_up, xa, hs_v)
+            base = b["tmp"][:rows]
+            O.gemv(self.sh_down, hs_v, base)
+            if self.sh_gate_w is not None:
+                O.router_logits(self.sh_gate_w, xa, b["glog"][:rows])
+                base.mul_(torch.sigmoid(b["glog"][:rows]))
+        K.moe_gemv(self.w_down.fmt, 2, self.w_down.planes, [], H, self.w_down.K, ne, k, b["counts"], b["offsets"],
+                   b["sorted"], b["h"].q, b["h"].d, b["h"].s, None, None, None, None, b["weights"][:rows].reshape(-1),
+                   O.PDL, e_lo=self.e_lo, T=rows, push_table=tp.push_recv[site], push_epoch=tp.epoch, base=base)
+
+    def shard(self, rank: int, world: int) -> "MoEFFN":
+        """Rank ``rank``'s expert-parallel shard: experts split across ranks (whole), router
+        replicated, the shared expert split by FFN row (gate / up rows, down columns)."""
+        from ..parallel.tp import cols
+        E, H, Fe = self.cfg.n_experts, self.cfg.hidden, self.cfg.expert_ffn
+        if E % world:
+            raise ValueError(f"{E} experts do not split over {world} ranks")
+        ne = E // world
+        lo = rank * ne
+
+        def own(w: QWeight, rows_per_expert: int) -> QWeight:
+            v = w.rows(lo * rows_per_expert, ne * rows_per_expert)
+            return QWeight(v.fmt, v.N, v.K, [p.contiguous() for p in v.planes])
+
+        f = MoEFFN(self.cfg, self.router_w, own(self.w_gate, Fe), own(self.w_up, Fe), own(self.w_down, H),
+                   router_bias=self.router_bias, sh_gate_w=self.sh_gate_w, e_lo=lo, n_local=ne)
+        if self.sh_down is not None:
+            Fs = self.sh_gate.N
+            if Fs % (32 * world):
+                raise ValueError(f"shared expert FFN {Fs} must split into 32-row blocks over {world} ranks")
+            lF = Fs // world
+            g, u = self.sh_gate.rows(rank * lF, lF), self.sh_up.rows(rank * lF, lF)
+            f._set_shared(QWeight(g.fmt, g.N, g.K, [p.contiguous() for p in g.planes]),
+                          QWeight(u.fmt, u.N, u.K, [p.contiguous() for p in u.planes]),
+                          cols(self.sh_down, rank * lF, (rank + 1) * lF))
+        return f
+
+    @staticmethod
+    def random_shard(cfg: ModelConfig, rank: int, world: int, device, g: torch.Generator, g_rep: torch.Generator,
+                     std: float = 0.02) -> "MoEFFN":
+        """Random-init weights generated directly in rank ``rank``'s expert-parallel shard shapes
+        (``g_rep`` seeds the replicated router identically on every rank)."""
+        fmt = type_id(cfg.weight_type)
+        E, H, Fe = cfg.n_experts, cfg.hidden, cfg.expert_ffn
+        ne = E // world
+        router = torch.randn(E, H, generator=g_rep, device=device) * std
+        f = MoEFFN(cfg, router, QWeight.random(fmt, ne * Fe, H, std, g, device),
+                   QWeight.random(fmt, ne * Fe, H, std, g, device), QWeight.random(fmt, ne * H, Fe, std, g, device),
+                   e_lo=rank * ne, n_local=ne)
+        if cfg.router == "sigmoid_bias":
+            f.router_bias = torch.zeros(E, device=device)
+        if cfg.shared_ffn:
+            lF = cfg.shared_ffn // world
+            f._set_shared(QWeight.random(fmt, lF, H, std, g, device), QWeight.random(fmt, lF, H, std, g, device),
+                          QWeight.random(fmt, H, lF, std, g, device))
+            if cfg.shared_gate:
+                f.sh_gate_w = torch.randn(1, H, generator=g_rep, device=device) * std
+        return f
 
     def forward(self, model, rows: int):
         """x[:rows] += MoE(q8 input model.xa[:rows]) on the device."""

@@ -30,11 +30,17 @@ from ..ops.qweight import QWeight
 
 
 def local_config(cfg: ModelConfig, world: int) -> ModelConfig:
+    """This rank's shard of the config: heads and dense FFN divided; MoE experts stay global (the
+    router scores all of them; each rank holds E / world of them, see MoEFFN.shard), the shared
+    expert's FFN divided."""
     if cfg.n_heads % world or cfg.n_kv_heads % world or cfg.ffn % (32 * world):
         raise ValueError(f"heads {cfg.n_heads}/{cfg.n_kv_heads} and ffn {cfg.ffn} must split over {world} ranks")
     if cfg.vocab % world:
         raise ValueError(f"vocab {cfg.vocab} must split over {world} ranks")
-    return cfg.with_(n_heads=cfg.n_heads // world, n_kv_heads=cfg.n_kv_heads // world, ffn=cfg.ffn // world)
+    if cfg.n_experts and cfg.n_experts % world:
+        raise ValueError(f"{cfg.n_experts} experts must split over {world} ranks")
+    return cfg.with_(n_heads=cfg.n_heads // world, n_kv_heads=cfg.n_kv_heads // world, ffn=cfg.ffn // world,
+                     shared_ffn=cfg.shared_ffn // world)
 
 
 def cols(w: QWeight, k0: int, k1: int) -> QWeight:
@@ -60,8 +66,6 @@ def shard_llama_weights(w, cfg: ModelConfig, rank: int, world: int):
     lnh, lnkv, lF = nh // world, nkv // world, F // world
     layers = []
     for lw in w.layers:
-        if lw.moe is not None:
-            raise NotImplementedError("tensor-parallel MoE layers: use expert parallelism")
         qkv = lw.wqkv[0] if len(lw.wqkv) == 1 else cat_rows(lw.wqkv)
         q = qkv.rows(rank * lnh * hd, lnh * hd)
         k = qkv.rows(nh * hd + rank * lnkv * hd, lnkv * hd)
@@ -74,6 +78,10 @@ def shard_llama_weights(w, cfg: ModelConfig, rank: int, world: int):
                                      b[nh * hd + rank * lnkv * hd:nh * hd + (rank + 1) * lnkv * hd],
                                      b[(nh + nkv) * hd + rank * lnkv * hd:(nh + nkv) * hd + (rank + 1) * lnkv * hd]])
         nl.q_norm, nl.k_norm = lw.q_norm, lw.k_norm
+        if lw.moe is not None:  # expert parallel: whole experts per rank, router replicated
+            nl.moe = lw.moe.shard(rank, world)
+            layers.append(nl)
+            continue
         gate, up = lw.w_gate.rows(rank * lF, lF), lw.w_up.rows(rank * lF, lF)
         nl.w_gu = cat_rows([gate, up])
         nl.w_gate, nl.w_up = nl.w_gu.rows(0, lF), nl.w_gu.rows(lF, lF)
@@ -98,10 +106,17 @@ def random_llama_weights_tp(cfg: ModelConfig, rank: int, world: int, device, see
     def W(N, K, f=fmt):
         return QWeight.random(f, N, K, std, g, device)
 
+    g_rep = torch.Generator(device=device)
+    g_rep.manual_seed(seed * 1009 + 5555)  # replicated MoE routers: identical on every rank
     layers = []
-    for _ in range(cfg.layers):
+    for l in range(cfg.layers):
         lw = LayerWeights(attn_norm=torch.ones(H, device=device), wqkv=[W((lnh + 2 * lnkv) * hd, H)],
                           wo=W(H, lnh * hd), ffn_norm=torch.ones(H, device=device))
+        if cfg.layer_is_moe(l):
+            from ..models.moe import MoEFFN
+            lw.moe = MoEFFN.random_shard(cfg, rank, world, device, g, g_rep, std)
+            layers.append(lw)
+            continue
         gu = W(2 * lF, H)
         lw.w_gu, lw.w_gate, lw.w_up = gu, gu.rows(0, lF), gu.rows(lF, lF)
         lw.w_down = W(H, lF)

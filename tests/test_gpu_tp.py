@@ -77,3 +77,58 @@ def test_tp2_matches_tp1(tiny_gguf, tmp_path):
     assert r["agree"] >= 0.9, r
     assert r["gens"][0] == r["gens"][1]  # every rank decodes the same tokens
     assert r["gens"][0][0] == r["ref_gen"][0]
+
+
+def _moe_worker(rank, world, port, shared, out_path):
+    import datetime
+
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        from hawking_b200.engine.engine import Engine
+        from hawking_b200.models.config import ModelConfig
+        from hawking_b200.models.llama import random_llama_weights
+        from hawking_b200.parallel.tp import TPComm, local_config, shard_llama_weights
+        cfg = ModelConfig(arch="mixtral", vocab=1024, hidden=512, layers=2, n_heads=8, n_kv_heads=2, head_dim=64,
+                          ffn=1024, n_experts=4, top_k=2, expert_ffn=512, weight_type="Q8_0", max_ctx=128)
+        if shared:  # Qwen-MoE style: a sigmoid-gated shared expert next to the routed ones
+            cfg = cfg.with_(shared_ffn=256, shared_gate=True, n_shared_experts=1, norm_topk=True)
+        w = random_llama_weights(cfg, dev, seed=4, std=0.05)  # same seed: identical on every rank
+        tp = TPComm(rank, world, 2 * cfg.layers, 8, cfg.hidden, dev)
+        eng = Engine.build(local_config(cfg, world), shard_llama_weights(w, cfg, rank, world), device=dev,
+                           max_batch=2, max_ctx=128, block_size=16, num_blocks=64, max_rows=8, tp=tp)
+        toks = list(range(10, 22))
+        local = eng.model.forward_tokens(toks, seq_id=1)
+        parts = [torch.empty_like(local) for _ in range(world)]
+        dist.all_gather(parts, local.contiguous())
+        full = torch.cat(parts, 1)
+        tp.check()
+        if rank == 0:
+            ref = Engine.build(cfg, w, device=dev, max_batch=2, max_ctx=128, block_size=16, num_blocks=64, max_rows=8)
+            ref.model.long_runs = False
+            ref_logits = torch.cat([ref.model.forward_tokens(toks[:8], seq_id=1),
+                                    ref.model.forward_tokens(toks[8:], seq_id=1, start_pos=8)])
+            err = float((full - ref_logits).abs().max() / ref_logits.abs().max())
+            torch.save({"err": err}, out_path)
+        torch.cuda.synchronize()
+        tp.close()
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("shared", [False, True])
+def test_tp2_expert_parallel_moe_matches_tp1(shared, tmp_path):
+    """Mixtral-style MoE (and a gated shared expert) with TP attention and experts split 2 + 2."""
+    import torch.multiprocessing as mp
+    out = str(tmp_path / "moe.pt")
+    mp.spawn(_moe_worker, args=(2, _free_port(), shared, out), nprocs=2, join=True)
+    r = torch.load(out)
+    assert r["err"] < 0.03, r
