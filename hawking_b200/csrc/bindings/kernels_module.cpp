@@ -41,8 +41,17 @@ void gemv(int64_t fmt, int64_t epi, const std::vector<Tensor>& w0, const std::ve
           const optional<Tensor>& y, const optional<Tensor>& bias, const optional<Tensor>& oq,
           const optional<Tensor>& od, const optional<Tensor>& os, const optional<Tensor>& x_f32,
           const optional<Tensor>& norm_w, double eps, bool pdl, const optional<Tensor>& argmax_slots,
-          int64_t argmax_offset, const optional<Tensor>& push_recv, const optional<Tensor>& push_epoch) {
+          int64_t argmax_offset, const optional<Tensor>& push_recv, const optional<Tensor>& push_epoch,
+          const std::vector<Tensor>& prefetch) {
   hk::GemvArgs a{};
+  TORCH_CHECK(prefetch.size() <= 8, "gemv: at most 8 prefetch ranges");
+  for (const Tensor& t : prefetch) {
+    TORCH_CHECK(t.is_cuda() && t.is_contiguous(), "gemv: prefetch ranges must be contiguous CUDA tensors");
+    TORCH_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, "gemv: prefetch ranges must be 16-byte aligned");
+    a.pf_ptr[a.pf_n] = reinterpret_cast<const uint8_t*>(t.data_ptr());
+    a.pf_bytes[a.pf_n] = (int64_t)t.numel() * t.element_size();
+    ++a.pf_n;
+  }
   int nb;
   if (x_f32.has_value()) {
     check_cuda(*x_f32, "x_f32");
@@ -296,7 +305,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("oq") = py::none(), py::arg("od") = py::none(), py::arg("os") = py::none(),
         py::arg("x_f32") = py::none(), py::arg("norm_w") = py::none(), py::arg("eps") = -1.0,
         py::arg("pdl") = false, py::arg("argmax_slots") = py::none(), py::arg("argmax_offset") = 0,
-        py::arg("push_recv") = py::none(), py::arg("push_epoch") = py::none());
+        py::arg("push_recv") = py::none(), py::arg("push_epoch") = py::none(),
+        py::arg("prefetch") = std::vector<Tensor>{});
   m.def("rmsnorm_q8", &rmsnorm_q8, py::arg("x"), py::arg("w"), py::arg("eps"), py::arg("norm"), py::arg("xq"),
         py::arg("xd"), py::arg("xs"), py::arg("y") = py::none(), py::arg("pdl") = false);
   m.def("rmsnorm", &rmsnorm, py::arg("x"), py::arg("w"), py::arg("eps"), py::arg("yf") = py::none(),

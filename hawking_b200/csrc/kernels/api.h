@@ -62,6 +62,12 @@ struct GemvArgs {
   unsigned long long* const* push_recv;
   const int* push_epoch;
   int push_n;
+  // L2 prefetch of the NEXT kernel's weights (up to kPrefetchRanges byte ranges): every CTA issues
+  // bulk L2 prefetches for its share before waiting on the previous kernel, so the chain of decode
+  // GEMVs streams weights from HBM continuously and each kernel finds its own weights in L2.
+  const uint8_t* pf_ptr[8];
+  int64_t pf_bytes[8];
+  int pf_n;
 };
 constexpr int kArgmaxSlots = 256;
 

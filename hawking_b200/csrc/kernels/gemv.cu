@@ -176,6 +176,22 @@ __device__ __forceinline__ void norm_q8_to_smem(const GemvArgs& a, int nb, int8_
 // SWIGLU_Q8 launches clusters of 4 CTAs: their 4 x 8 rows form one 32-element q8 block of the
 // output, which the cluster's first CTA quantises after reading the other CTAs' values through
 // distributed shared memory.
+// This CTA's share of the next kernel's weights, prefetched into L2 by warp 0 in pieces of <= 4 KB
+// (cp.async.bulk.prefetch: 16-byte aligned starts and sizes; nothing is written, no completion).
+__device__ __forceinline__ void prefetch_next_weights(const GemvArgs& a) {
+  if (threadIdx.x >= 32) return;
+  const int lane = threadIdx.x;
+  for (int r = 0; r < a.pf_n; ++r) {
+    const int64_t total = a.pf_bytes[r];
+    const int64_t per = (((total + gridDim.x - 1) / gridDim.x) + 15) & ~int64_t(15);
+    const int64_t s0 = (int64_t)blockIdx.x * per, s1 = min(total, s0 + per);
+    for (int64_t off = s0 + (int64_t)lane * 4096; off < s1; off += 32 * 4096) {
+      const uint32_t len = (uint32_t)min((int64_t)4096, s1 - off) & ~15u;
+      if (len) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a.pf_ptr[r] + off), "r"(len) : "memory");
+    }
+  }
+}
+
 template <int FMT, int NB, int EPI, int XIN>
 __global__ void __launch_bounds__(256, (NB == 1 && XIN == XIN_Q8) ? (EPI == EPI_SWIGLU_Q8 ? 3 : 4) : 1) gemv_kernel(GemvArgs a, int nb) {
   extern __shared__ __align__(16) uint8_t gsm[];
@@ -195,6 +211,7 @@ __global__ void __launch_bounds__(256, (NB == 1 && XIN == XIN_Q8) ? (EPI == EPI_
     load_round<FMT>(a.w0, row, 0, n_units, wg);
     if constexpr (EPI == EPI_SWIGLU_Q8) load_round<FMT>(a.w1, row, 0, n_units, wu);
   }
+  if (a.pf_n) prefetch_next_weights(a);
   pdl_wait();
 
   // 2) activations into shared memory (granule-swizzled, see swz_granule)

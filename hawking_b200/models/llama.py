@@ -316,12 +316,15 @@ class LlamaModel:
                     ops.rmsnorm_q8(x, lw.ffn_norm, cfg.eps, self.xa.view(rows))
                     lw.moe.forward(self, rows)
                 else:
+                    nxt = w.layers[l + 1].wqkv if l + 1 < len(w.layers) else None
                     ops.rmsnorm_q8(x, lw.ffn_norm, cfg.eps, self.xa.view(rows))
                     self._gemv_cols(lambda c0, c1: ops.gemv_swiglu(lw.w_gate, lw.w_up, self.xa_view(c0, c1),
-                                                                   self._q8_slice(self.hq, c0, c1)), rows)
+                                                                   self._q8_slice(self.hq, c0, c1),
+                                                                   prefetch=[lw.w_down] if c0 == 0 else None), rows)
                     self._gemv_cols(lambda c0, c1: ops.gemv(lw.w_down,
                                                             self._q8_slice(self.hq, c0, c1, lw.w_down.K),
-                                                            x[c0:c1], residual=True), rows)
+                                                            x[c0:c1], residual=True,
+                                                            prefetch=nxt if c0 == 0 else None), rows)
         if n_logits < 0:  # no row of this chunk is sampled
             if advance:
                 ops.advance(inp.ids, self.next_ids, inp.positions, inp.row_ctx, rows)
@@ -385,13 +388,15 @@ class LlamaModel:
         def qkv_fn(c0, c1):
             xa = self.xa_view(c0, c1)
             off = 0
-            for wt in lw.wqkv:
-                ops.gemv(wt, xa, self.qkv[c0:c1, off:off + wt.N])
+            for i, wt in enumerate(lw.wqkv):
+                last = i == len(lw.wqkv) - 1 and c0 == 0
+                ops.gemv(wt, xa, self.qkv[c0:c1, off:off + wt.N], prefetch=[lw.wo] if last else None)
                 off += wt.N
         self._gemv_cols(qkv_fn, rows)
         self._rope_attention(l, lw, rows, splits, out_q8=self.att.view(rows))
+        ffn_next = None if lw.moe is not None else ([lw.w_gu] if lw.w_gu is not None else [lw.w_gate, lw.w_up])
         self._gemv_cols(lambda c0, c1: ops.gemv(lw.wo, self._q8_slice(self.att, c0, c1), x[c0:c1],
-                                                residual=True), rows)
+                                                residual=True, prefetch=ffn_next if c0 == 0 else None), rows)
 
     # ---- tensor parallel (decode GEMV path: fused push all-reduce; see parallel/tp.py) ----
     def _layer_gemv_tp(self, l, lw, rows, splits):
@@ -404,17 +409,20 @@ class LlamaModel:
         # (for l > 0 the previous layer's FFN all-reduce already left norm(x) in self.xa)
         xa = self.xa_view(0, rows)
         off = 0
-        for wt in lw.wqkv:
-            ops.gemv(wt, xa, self.qkv[:rows, off:off + wt.N])
+        for i, wt in enumerate(lw.wqkv):
+            ops.gemv(wt, xa, self.qkv[:rows, off:off + wt.N], prefetch=[lw.wo] if i == len(lw.wqkv) - 1 else None)
             off += wt.N
         self._rope_attention(l, lw, rows, splits, out_q8=self.att.view(rows))
-        ops.gemv_push(lw.wo, self._q8_slice(self.att, 0, rows), tp, 2 * l)
+        ffn_next = None if lw.moe is not None else ([lw.w_gu] if lw.w_gu is not None else [lw.w_gate, lw.w_up])
+        ops.gemv_push(lw.wo, self._q8_slice(self.att, 0, rows), tp, 2 * l, prefetch=ffn_next)
         ops.tp_allreduce_rmsnorm_q8(tp, 2 * l, xa_res, xb_res, lw.ffn_norm, cfg.eps, self.xa.view(rows))
         if lw.moe is not None:  # expert parallel; the experts' combine is this site's push
             lw.moe.forward_ep(self, rows, 2 * l + 1)
         else:
-            ops.gemv_swiglu(lw.w_gate, lw.w_up, self.xa_view(0, rows), self._q8_slice(self.hq, 0, rows))
-            ops.gemv_push(lw.w_down, self._q8_slice(self.hq, 0, rows, lw.w_down.K), tp, 2 * l + 1)
+            nxt = w.layers[l + 1].wqkv if l + 1 < len(w.layers) else None
+            ops.gemv_swiglu(lw.w_gate, lw.w_up, self.xa_view(0, rows), self._q8_slice(self.hq, 0, rows),
+                            prefetch=[lw.w_down])
+            ops.gemv_push(lw.w_down, self._q8_slice(self.hq, 0, rows, lw.w_down.K), tp, 2 * l + 1, prefetch=nxt)
         nxt = w.layers[l + 1].attn_norm if l + 1 < len(w.layers) else w.out_norm
         ops.tp_allreduce_rmsnorm_q8(tp, 2 * l + 1, xb_res, xa_res, nxt, cfg.eps, self.xa.view(rows))
 

@@ -60,26 +60,48 @@ def rmsnorm(x, w, eps, yf=None, yb=None):
     kernels().rmsnorm(x, w, eps, yf, yb, PDL)
 
 
+def _prefetch_ranges(ws) -> list:
+    """Weight planes of ``ws`` (QWeights) as byte ranges for the GEMV's next-kernel L2 prefetch."""
+    if not ws or not PREFETCH_NEXT:
+        return []
+    out = []
+    for w in ws:
+        if w is None:
+            continue
+        for p in w.planes:
+            if p.is_contiguous() and p.data_ptr() % 16 == 0 and len(out) < 8:
+                out.append(p)
+    return out
+
+
+# Decode GEMVs can prefetch the next projection's weights into L2 (see GemvArgs.pf_ptr). Off by
+# default: on Llama-3-8B Q4_K bs1 decode it measured 4% slower (410.7 vs 427.8 tok/s); HK_PREFETCH=1
+# turns it on for A/B measurements.
+PREFETCH_NEXT = os.environ.get("HK_PREFETCH", "0") == "1"
+
+
 def gemv(w: QWeight, x: Q8Act, y: torch.Tensor, residual: bool = False, bias=None, argmax_slots=None,
-         argmax_offset: int = 0):
+         argmax_offset: int = 0, prefetch=None):
     """y[b] = W x[b] (or y += ... with ``residual``). ``argmax_slots`` (int64 [nb, 256], zeroed)
     additionally folds every output into packed greedy keys (row index + ``argmax_offset``);
-    ``argmax_finalize`` reads them."""
+    ``argmax_finalize`` reads them. ``prefetch``: the weights of the kernel that follows, pulled
+    into L2 while this one runs."""
     launches.add()
     kernels().gemv(w.fmt, EPI_RESID if residual else EPI_STORE, w.planes, [], w.N, w.K, x.q, x.d, x.s, y, bias,
-                   None, None, None, None, None, -1.0, PDL, argmax_slots, argmax_offset)
+                   None, None, None, None, None, -1.0, PDL, argmax_slots, argmax_offset,
+                   prefetch=_prefetch_ranges(prefetch))
 
 
 ARGMAX_SLOTS = 256
 EPI_PUSH = 3
 
 
-def gemv_push(w: QWeight, x: Q8Act, tp, site: int, bias=None):
+def gemv_push(w: QWeight, x: Q8Act, tp, site: int, bias=None, prefetch=None):
     """Row-parallel projection: the partial outputs go to every rank's receive region of ``site``
     (tensor-parallel all-reduce push, see parallel/tp.py)."""
     launches.add()
     kernels().gemv(w.fmt, EPI_PUSH, w.planes, [], w.N, w.K, x.q, x.d, x.s, None, bias, None, None, None, None, None,
-                   -1.0, PDL, None, 0, tp.push_recv[site], tp.epoch)
+                   -1.0, PDL, None, 0, tp.push_recv[site], tp.epoch, prefetch=_prefetch_ranges(prefetch))
 
 
 def tp_begin(tp):
@@ -109,10 +131,10 @@ def argmax_finalize(slots: torch.Tensor, rows: int, out: torch.Tensor):
     kernels().argmax_finalize(slots, rows, out, PDL)
 
 
-def gemv_swiglu(w_gate: QWeight, w_up: QWeight, x: Q8Act, out: Q8Act):
+def gemv_swiglu(w_gate: QWeight, w_up: QWeight, x: Q8Act, out: Q8Act, prefetch=None):
     launches.add()
     kernels().gemv(w_gate.fmt, EPI_SWIGLU_Q8, w_gate.planes, w_up.planes, w_gate.N, w_gate.K, x.q, x.d, x.s, None,
-                   None, out.q, out.d, out.s, None, None, -1.0, PDL)
+                   None, out.q, out.d, out.s, None, None, -1.0, PDL, prefetch=_prefetch_ranges(prefetch))
 
 
 def gemv_norm(w: QWeight, x: torch.Tensor, norm_w, eps: float, y: torch.Tensor, bias=None):
