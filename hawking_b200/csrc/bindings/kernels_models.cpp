@@ -372,6 +372,7 @@ void register_model_kernels(py::module_& m) {
         py::arg("block_tables"), py::arg("row_seq"), py::arg("rope"), py::arg("cache"), py::arg("pdl") = false);
   m.def("mla_absorb_q", &mla_absorb_q, py::arg("q"), py::arg("w_uk"), py::arg("positions"), py::arg("rope"),
         py::arg("q_lat"), py::arg("q_pe"), py::arg("pdl") = false);
+  m.def("mla_heads_per_cta", &hk::mla_heads_per_cta, py::arg("nh"), py::arg("rows"));
   m.def("mla_decode", &mla_decode, py::arg("q_lat"), py::arg("q_pe"), py::arg("cache"), py::arg("block_tables"),
         py::arg("row_seq"), py::arg("row_ctx"), py::arg("scale"), py::arg("num_splits"), py::arg("o_lat"),
         py::arg("status"), py::arg("pdl") = false);

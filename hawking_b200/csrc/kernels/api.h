@@ -508,6 +508,7 @@ struct MlaDecodeArgs {
   float* o_lat;               // [R, nh, 512]
   int* status;
 };
+int mla_heads_per_cta(int nh, int rows);  // heads sharing one CTA in mla_decode
 void mla_decode_launch(MlaDecodeArgs a, cudaStream_t s, bool pdl);
 struct MlaOutArgs {
   const float* o_lat;

@@ -418,9 +418,24 @@ __global__ void __launch_bounds__(WARPS * 32) mla_decode_kernel(MlaDecodeArgs a)
   cluster.sync();
 }
 
+int mla_heads_per_cta(int nh, int rows) {
+  // 4 heads share each latent row a CTA stages, unless that leaves too few CTAs (tensor-parallel
+  // shards hold nh / N heads): then 2 or 1, trading latent re-reads (L2) for parallelism
+  if (nh % 4 == 0 && rows * (nh / 4) >= 16) return 4;
+  if (nh % 2 == 0 && rows * (nh / 2) >= 16) return 2;
+  return 1;
+}
+
+template <int G>
+static void mla_decode_go(const MlaDecodeArgs& a, size_t smem, cudaStream_t s, bool pdl) {
+  constexpr int WARPS = 8;
+  auto kern = mla_decode_kernel<G, WARPS>;
+  HK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  launch_cluster(kern, dim3(a.num_splits, a.nh / G, a.R), dim3(WARPS * 32), smem, s, pdl, a.num_splits, a);
+}
+
 void mla_decode_launch(MlaDecodeArgs a, cudaStream_t s, bool pdl) {
-  constexpr int G = 4, WARPS = 8;
-  if (a.nh % G) throw std::runtime_error("mla: heads must be a multiple of 4");
+  const int G = mla_heads_per_cta(a.nh, a.R);
   if (a.num_splits != 1 && a.num_splits != 2 && a.num_splits != 4 && a.num_splits != 8)
     throw std::runtime_error("mla: num_splits must be 1, 2, 4 or 8");
   const int slab_bytes = a.block_size * kMlaRow * 2;
@@ -430,9 +445,9 @@ void mla_decode_launch(MlaDecodeArgs a, cudaStream_t s, bool pdl) {
   if (ns < 1 || (ns < most && ns < 2)) throw std::runtime_error("mla: latent block too large for the ring");
   a.stage_blocks = ns;
   const size_t smem = 128 + (size_t)ns * slab_bytes;
-  auto kern = mla_decode_kernel<G, WARPS>;
-  HK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  launch_cluster(kern, dim3(a.num_splits, a.nh / G, a.R), dim3(WARPS * 32), smem, s, pdl, a.num_splits, a);
+  if (G == 4) mla_decode_go<4>(a, smem, s, pdl);
+  else if (G == 2) mla_decode_go<2>(a, smem, s, pdl);
+  else mla_decode_go<1>(a, smem, s, pdl);
 }
 
 }  // namespace hk

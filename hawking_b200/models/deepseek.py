@@ -192,8 +192,11 @@ class DeepSeekModel:
         self.launches_per_graph = 0
 
     def num_splits(self, rows: int) -> int:
+        """KV splits (cluster size, <= 8) so that splits x head groups x rows covers the SMs; the
+        kernel groups 4, 2 or 1 heads per CTA (fewer for tensor-parallel head shards)."""
+        groups = self.cfg.n_heads // kernels().mla_heads_per_cta(self.cfg.n_heads, rows)
         s = 1
-        while s < 8 and rows * (self.cfg.n_heads // 4) * s < 148:
+        while s < 8 and rows * groups * s < 148:
             s *= 2
         return s
 

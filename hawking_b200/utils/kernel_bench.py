@@ -67,6 +67,8 @@ def build_cases(dev: str = "cuda", ctx: int = 2048, rows: int = 1, only=None, bn
     cases = {}
     if only is not None and all(c.startswith("tc_") or c == "attention_prefill" for c in only):
         return _tc_cases(dev, ctx, rows, g, only, bn)
+    if only is not None and all(c.startswith("mla_decode") for c in only):
+        return _mla_cases(dev, ctx, rows, g)
     wo, wd, wqkv, wgu = copies((H, H)), copies((H, F)), copies((6144, H)), copies((F, H), (F, H))
     x = torch.randn(rows, H, device=dev)
     nw = torch.ones(H, device=dev)
@@ -114,6 +116,33 @@ def build_cases(dev: str = "cuda", ctx: int = 2048, rows: int = 1, only=None, bn
     wl = w(V, H)
     logits = torch.zeros(rows, V, device=dev)
     cases["lm_head"] = (lambda i: ops.gemv(wl, xa, logits), wl.nbytes)
+    return cases
+
+
+def _mla_cases(dev, ctx, rows, g):
+    """Absorbed MLA decode over a ``ctx``-token bf16 latent cache (576 per token): all 64 heads of
+    the DeepSeek-V3-style config (one GPU) and the 8 heads of one rank at TP8."""
+    from hawking_b200._ext import kernels
+    K = kernels()
+    bs = 64
+    nblk = (ctx + bs - 1) // bs
+    cache = torch.randn(nblk * rows, bs, 576, device=dev).bfloat16()
+    tables = torch.arange(nblk * rows, dtype=torch.int32, device=dev).view(rows, nblk).contiguous()
+    rs = torch.arange(rows, dtype=torch.int32, device=dev)
+    rc = torch.full((rows,), ctx, dtype=torch.int32, device=dev)
+    st = torch.zeros(1, dtype=torch.int32, device=dev)
+    cases = {}
+    for nh in (64, 8):
+        ql, qp = torch.randn(rows, nh, 512, device=dev), torch.randn(rows, nh, 64, device=dev)
+        o = torch.zeros(rows, nh, 512, device=dev)
+        groups = nh // K.mla_heads_per_cta(nh, rows)
+        splits = 1
+        while splits < 8 and rows * groups * splits < 148:
+            splits *= 2
+        cases[f"mla_decode_h{nh}"] = (
+            lambda i, ql=ql, qp=qp, o=o, splits=splits: K.mla_decode(ql, qp, cache, tables, rs, rc, 0.07, splits, o, st,
+                                                                     True),
+            rows * ctx * 576 * 2, 2.0 * rows * ctx * nh * (576 + 512))
     return cases
 
 

@@ -44,3 +44,33 @@ def test_deepseek_matches_torch_oracle():
     err = float((got - ref).abs().max() / ref.abs().max())
     assert err < 0.03, err
     assert int(m.status.item()) == 0
+
+
+@pytest.mark.parametrize("nh,rows", [(64, 1), (8, 1), (8, 3), (4, 2), (16, 8)])
+def test_mla_decode_head_groupings(nh, rows):
+    """Latent-cache attention for every heads-per-CTA grouping (4, 2, 1) vs fp32 PyTorch."""
+    from hawking_b200._ext import kernels
+    K = kernels()
+    g = torch.Generator(device=DEV).manual_seed(nh * 10 + rows)
+    bs, nblk, ctx = 64, 6, 300
+    cache = (torch.randn(nblk * rows, bs, 576, generator=g, device=DEV)).bfloat16()
+    tables = torch.arange(nblk * rows, dtype=torch.int32, device=DEV).view(rows, nblk).contiguous()
+    row_seq = torch.arange(rows, dtype=torch.int32, device=DEV)
+    row_ctx = torch.tensor([ctx - 7 * r for r in range(rows)], dtype=torch.int32, device=DEV)
+    q_lat = torch.randn(rows, nh, 512, generator=g, device=DEV) * 0.05
+    q_pe = torch.randn(rows, nh, 64, generator=g, device=DEV) * 0.05
+    o = torch.zeros(rows, nh, 512, device=DEV)
+    st = torch.zeros(1, dtype=torch.int32, device=DEV)
+    scale = 192 ** -0.5
+    splits = 1
+    groups = nh // K.mla_heads_per_cta(nh, rows)
+    while splits < 8 and rows * groups * splits < 148:
+        splits *= 2
+    K.mla_decode(q_lat, q_pe, cache, tables, row_seq, row_ctx, scale, splits, o, st, False)
+    torch.cuda.synchronize()
+    assert int(st.item()) == 0
+    for r in range(rows):
+        c = cache[tables[r].long()].reshape(-1, 576)[: int(row_ctx[r])].float()
+        sc = (q_lat[r] @ c[:, :512].T + q_pe[r] @ c[:, 512:].T) * scale
+        ref = torch.softmax(sc, -1) @ c[:, :512]
+        torch.testing.assert_close(o[r], ref, rtol=2e-3, atol=2e-3)
