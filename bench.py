@@ -43,6 +43,9 @@ def parse():
     ap.add_argument("--bs64", type=int, default=1, help="also time batch-64 decode (1/0)")
     ap.add_argument("--ttft-runs", type=int, default=3)
     ap.add_argument("--e2e-steps", type=int, default=0, help="0 = same as --steps")
+    ap.add_argument("--e2e-ctx", type=int, default=256,
+                    help="prompt length of the end-to-end run of the MLA / hybrid models (their prompts prefill in "
+                         "8-token chunks / token by token)")
     ap.add_argument("--layers", type=int, default=0, help="override layer count (debug only; invalidates the number)")
     ap.add_argument("--parallel", default="tp", choices=["tp", "dp"],
                     help="N > 1: tensor parallel over the N GPUs (one model, strong scaling) or data-parallel replicas")
@@ -66,6 +69,49 @@ def reference_unavailable(args):
     print(json.dumps(line))
 
 
+def engine_e2e(eng, vocab: int, prompt_len: int, K: int, W: int, world: int, dev):
+    """End-to-end decode through the public Engine API for the MLA / hybrid models: one request
+    with a ``prompt_len``-token random prompt (its TTFT is returned too), then K timed
+    Engine.step() calls, each uploading the step's inputs from pinned memory and reading the
+    sampled id back (max over ranks)."""
+    import torch
+    import torch.distributed as dist
+    from hawking_b200.engine.sampling import SamplingParams
+    from hawking_b200.formats.synth import random_prompt
+    prompt = random_prompt(prompt_len, vocab, seed=100)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t_a = time.perf_counter()
+    rid = eng.add_request(prompt, SamplingParams(max_tokens=K + W + 1))
+    while not eng.requests[rid].output:
+        eng.step()
+    ttft = (time.perf_counter() - t_a) * 1000.0
+    for _ in range(W):
+        eng.step()
+    st = eng.stats
+    h0, d0 = st.h2d_bytes, st.d2h_bytes
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t_e = time.perf_counter()
+    n0 = len(eng.requests[rid].output)
+    for _ in range(K):
+        eng.step()
+    torch.cuda.synchronize()
+    dt = time.perf_counter() - t_e
+    n_tok = len(eng.requests[rid].output) - n0
+    if world > 1:
+        t = torch.tensor([dt], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dt = t.item()
+    while eng.has_work():
+        eng.step()
+    return ({"value": round(n_tok / dt, 2), "unit": "tok/s", "h2d_bytes_per_step": (st.h2d_bytes - h0) // max(1, K),
+             "d2h_bytes_per_step": (st.d2h_bytes - d0) // max(1, K), "api": "Engine.step()",
+             "context": prompt_len}, round(ttft, 2))
+
+
 def bench_qwen_next(args):
     """Qwen3-Next-style hybrid (config 4): bs1 / bs8 device-timed decode on one GPU, 80B-parameter
     random weights in the mixed <= 1.5 BPW recipe (random codes + Gaussian-statistics scales)."""
@@ -86,7 +132,8 @@ def bench_qwen_next(args):
     n_full = sum(cfg.layer_is_full_attention(l) for l in range(cfg.layers))
     bs, max_seqs = 64, 8
     max_blocks = -(-cfg.max_ctx // bs)
-    kv = PagedKVCache(n_full, cfg.n_kv_heads, cfg.head_dim, max_seqs * max_blocks + 8, bs, max_seqs, max_blocks, dev)
+    kv = PagedKVCache(n_full, cfg.n_kv_heads, cfg.head_dim, max_seqs * max_blocks + 8, bs, max_seqs, max_blocks, dev,
+                      prefix_cache=False)
     m = QwenNextModel(cfg, w, kv, max_rows=8, max_seqs=max_seqs, device=dev)
     g = torch.Generator(device=dev).manual_seed(1)
     for l in range(n_full):
@@ -129,6 +176,9 @@ def bench_qwen_next(args):
     ms1, clocks = timed(1)
     launches = m.launches_per_graph
     ms8, clocks8 = timed(8)
+    from hawking_b200.engine.engine import Engine
+    eng = Engine(cfg, m, kv, max_batch=max_seqs - 1, max_prefill_tokens=8)
+    e2e, ttft = engine_e2e(eng, cfg.vocab, args.e2e_ctx, K, W, 1, dev)
     out = {
         "metric": "decode tok/s bs1 (Qwen3-Next-style hybrid MoE, .gravity mixed <= 1.5 BPW), 1 GPU",
         "value": round(1000.0 / ms1, 2), "unit": "tok/s", "n_gpus": 1, "steps": K, "warmup": W,
@@ -143,7 +193,8 @@ def bench_qwen_next(args):
                    "global_batch": 1, "seq_len": ctx, "parallelism": "tp1",
                    "complete_bpw": round(complete_bpw, 3),
                    "l2": "inputs larger than L2: %.1f GB of weights resident" % ((w.table.nbytes + w.embed.nbytes) / 1e9)},
-        "clocks": clocks, "e2e": None, "e2e_note": "no engine/scheduler integration for the hybrid model yet",
+        "clocks": clocks, "e2e": e2e, "ttft_ms": ttft, "ttft_prompt": args.e2e_ctx,
+        "ttft_note": "prompts prefill token by token (no chunked DeltaNet prefill yet)",
         "gpu_launches": launches * K,
         "bs8": {"tok_s_aggregate": round(8 * 1000.0 / ms8, 1), "ms_per_step": round(ms8, 4), "clocks": clocks8},
         "weights_gb": round((w.table.nbytes + w.embed.nbytes) / 1e9, 2),
@@ -256,9 +307,12 @@ def bench_deepseek(args):
     ms1, clocks = timed(1)
     launches = m.launches_per_graph
     ms8, clocks8 = timed(8)
+    from hawking_b200.engine.engine import Engine
+    eng = Engine(mcfg, m, kv, max_batch=8, max_prefill_tokens=8)
+    e2e, ttft = engine_e2e(eng, cfg.vocab, args.e2e_ctx, K, W, world, dev)
     if tp is not None:
         tp.check()
-        m.release_graphs() if hasattr(m, "release_graphs") else m._graphs.clear()
+        m._graphs.clear()
         tp.close()
     out = {
         "metric": "decode tok/s bs1 (DeepSeek-V3-style MLA + MoE, fp8 e4m3 block-scaled), %d GPU" % world,
@@ -274,7 +328,8 @@ def bench_deepseek(args):
                    "global_batch": 1, "seq_len": ctx,
                    "parallelism": "tp1" if world == 1 else "tp%d attention + ep%d experts" % (world, world),
                    "l2": "inputs larger than L2: %.1f GB of weights resident per GPU" % (w.nbytes / 1e9)},
-        "clocks": clocks, "e2e": None, "e2e_note": "no engine/scheduler integration for the MLA model yet",
+        "clocks": clocks, "e2e": e2e,
+        "ttft_ms": ttft, "ttft_prompt": args.e2e_ctx,
         "gpu_launches": launches * K,
         "bs8": {"tok_s_aggregate": round(8 * 1000.0 / ms8, 1), "ms_per_step": round(ms8, 4), "clocks": clocks8},
         "weights_gb": round(w.nbytes / 1e9, 2), "load_s": round(t_load, 1),

@@ -85,6 +85,44 @@ class Engine:
         return Engine(cfg, model, kv, max_batch=max_batch, max_prefill_tokens=max_prefill_tokens, policy=policy)
 
     @staticmethod
+    def build_deepseek(cfg: ModelConfig, weights, device="cuda", max_batch: int = 8, max_ctx: Optional[int] = None,
+                       block_size: int = 64, num_blocks: Optional[int] = None, kv_fraction: float = 0.5,
+                       policy: int = 0, tp=None):
+        """Engine around the MLA + MoE model (paged latent cache; forwards of <= 8 rows, several
+        rows of one sequence allowed: prompts prefill in 8-token chunks)."""
+        from ..models.deepseek import LAT, ROPE, DeepSeekModel, LatentCache
+        max_ctx = max_ctx or cfg.max_ctx
+        max_blocks = -(-max_ctx // block_size)
+        if num_blocks is None:
+            free, _ = torch.cuda.mem_get_info(device)
+            bpb = cfg.layers * block_size * (LAT + ROPE) * 2
+            num_blocks = min(int(free * kv_fraction // bpb), (max_batch + 1) * max_blocks + 16)
+        kv = LatentCache(cfg.layers, num_blocks, block_size, max_batch + 1, max_blocks, device)
+        model = DeepSeekModel(cfg, weights, kv, max_rows=8, device=device, tp=tp)
+        return Engine(cfg, model, kv, max_batch=max_batch, max_prefill_tokens=8, policy=policy)
+
+    @staticmethod
+    def build_qwen_next(cfg: ModelConfig, weights, device="cuda", max_batch: int = 8, max_ctx: Optional[int] = None,
+                        block_size: int = 64, num_blocks: Optional[int] = None, kv_fraction: float = 0.5,
+                        policy: int = 0):
+        """Engine around the hybrid DeltaNet / gated-attention model: paged KV for the full-
+        attention layers, one recurrent-state slot per block-table row (reset when a sequence
+        starts), no prefix reuse (a cached prefix would not restore the recurrent state), and
+        one row per sequence per forward (the recurrence is sequential)."""
+        from ..models.qwen_next import QwenNextModel
+        max_ctx = max_ctx or cfg.max_ctx
+        max_blocks = -(-max_ctx // block_size)
+        n_full = sum(cfg.layer_is_full_attention(l) for l in range(cfg.layers))
+        if num_blocks is None:
+            free, _ = torch.cuda.mem_get_info(device)
+            bpb = PagedKVCache.bytes_per_block(max(1, n_full), cfg.n_kv_heads, cfg.head_dim, block_size)
+            num_blocks = min(int(free * kv_fraction // bpb), (max_batch + 1) * max_blocks + 16)
+        kv = PagedKVCache(max(1, n_full), cfg.n_kv_heads, cfg.head_dim, num_blocks, block_size, max_batch + 1,
+                          max_blocks, device, prefix_cache=False)
+        model = QwenNextModel(cfg, weights, kv, max_rows=8, max_seqs=max_batch + 1, device=device)
+        return Engine(cfg, model, kv, max_batch=max_batch, max_prefill_tokens=8 * max_batch, policy=policy)
+
+    @staticmethod
     def from_gguf(path: str, device="cuda", max_batch: int = 8, max_ctx: Optional[int] = None, **kw):
         """Load a GGUF model (weights re-laid for the kernels) and build an engine around it."""
         from ..formats.gguf import GgufModel
@@ -127,18 +165,45 @@ class Engine:
         ids, pos, slots, rseq, rctx, sample_rows = [], [], [], [], [], []
         live = [it.id for it in items]
         self.kv.sync_tables(live)
+        serial = getattr(m, "serial_rows", False)
+        R = getattr(m, "row_limit", m.max_rows)
+        per_item = []
         for it in items:
             toks = self.sched.tokens(it.id)
             r = self.kv.row(it.id)
+            if it.p0 == 0 and hasattr(m, "reset_state"):
+                m.reset_state(r)  # a new sequence on this row: fresh recurrent state
             sl = self.kv.bm.slots(it.id, it.p0, it.p1)
-            for p in range(it.p0, it.p1):
-                ids.append(toks[p])
-                pos.append(p)
-                rseq.append(r)
-                rctx.append(p + 1)
-            slots.extend(sl)
-            if it.sample:
-                sample_rows.append((it, len(ids) - 1))
+            per_item.append((it, toks, r, sl))
+        if not serial:
+            for it, toks, r, sl in per_item:
+                for p in range(it.p0, it.p1):
+                    ids.append(toks[p])
+                    pos.append(p)
+                    rseq.append(r)
+                    rctx.append(p + 1)
+                slots.extend(sl)
+                if it.sample:
+                    sample_rows.append((it, len(ids) - 1))
+            bounds = [(c0, min(len(ids), c0 + R)) for c0 in range(0, len(ids), R)]
+        else:
+            # waves of at most one row per sequence, in position order (each wave <= R rows)
+            bounds = []
+            longest = max(it.p1 - it.p0 for it in items)
+            for k in range(longest):
+                wave = [(it, toks, r, sl) for it, toks, r, sl in per_item if it.p0 + k < it.p1]
+                for w0 in range(0, len(wave), R):
+                    b0 = len(ids)
+                    for it, toks, r, sl in wave[w0:w0 + R]:
+                        p = it.p0 + k
+                        ids.append(toks[p])
+                        pos.append(p)
+                        rseq.append(r)
+                        rctx.append(p + 1)
+                        slots.append(sl[k])
+                        if it.sample and p == it.p1 - 1:
+                            sample_rows.append((it, len(ids) - 1))
+                    bounds.append((b0, len(ids)))
         n = len(ids)
         decode_only = all(it.p1 - it.p0 == 1 for it in items)
         if hasattr(m, "long_runs"):
@@ -146,9 +211,7 @@ class Engine:
         greedy = all(it.greedy for it, _ in sample_rows)
         mode = "greedy" if greedy else "none"
         sampled: List[int] = []
-        R = getattr(m, "row_limit", m.max_rows)
-        for c0 in range(0, n, R):
-            c1 = min(n, c0 + R)
+        for c0, c1 in bounds:
             self.stats.h2d_bytes += m.inp.upload(ids[c0:c1], pos[c0:c1], slots[c0:c1], rseq[c0:c1], rctx[c0:c1])
             rows_here = [(it, r - c0) for it, r in sample_rows if c0 <= r < c1]
             if self.use_graphs and decode_only and c1 - c0 == n:
@@ -169,6 +232,9 @@ class Engine:
                 picks = [(it, j) for j, (it, _) in enumerate(rows_here)] if 0 < k < c1 - c0 else rows_here
             if rows_here:
                 sampled.extend(self._sample(picks, greedy))
+        if serial and sample_rows:  # back to the plan's item order (rows ran in wave order)
+            by_id = {it.id: tok for (it, _), tok in zip(sample_rows, sampled)}
+            sampled = [by_id[it.id] for it in items if it.id in by_id]
         events = self.sched.commit(plan, sampled)
         now = time.perf_counter()
         out = []

@@ -190,6 +190,9 @@ class DeepSeekModel:
             self.argmax_slots = torch.zeros(R, ops.ARGMAX_SLOTS, dtype=torch.int64, device=dev)
         self._graphs = {}
         self.launches_per_graph = 0
+        engine_buffers(self, R)
+
+    row_limit = property(lambda self: self.max_rows)  # rows one forward takes (engine chunking)
 
     def num_splits(self, rows: int) -> int:
         """KV splits (cluster size, <= 8) so that splits x head groups x rows covers the SMs; the
@@ -280,9 +283,16 @@ class DeepSeekModel:
             mixed_gemv_swiglu(t, L.idx["sg"], L.idx["su"], xa, hs)
             mixed_gemv(t, L.idx["sd"], hs, self.x[:rows], residual=True)
 
-    def forward(self, rows: int, sample: str = "greedy", advance: bool = False):
+    def forward(self, rows: int, sample: str = "greedy", advance: bool = False, n_logits: int = 0):
+        """``n_logits`` (engine): > 0 moves the logits / greedy ids of ``logit_rows[:n_logits]`` to
+        the first rows (all rows are computed; at most 8)."""
         if self.tp is not None:
-            return self._forward_tp(rows, sample, advance)
+            self._forward_tp(rows, sample, advance)
+        else:
+            self._forward_local(rows, sample, advance)
+        compact_logit_rows(self, n_logits)
+
+    def _forward_local(self, rows: int, sample: str = "greedy", advance: bool = False):
         cfg, w, inp = self.cfg, self.w, self.inp
         ops.embed(w.embed, inp.ids[:rows], self.x[:rows])
         for l, L in enumerate(w.layers):
@@ -359,6 +369,23 @@ class DeepSeekModel:
             self.launches_per_graph = ops.launches.n - n0
             self._graphs[key] = g
         g.replay()
+
+
+def engine_buffers(model, R: int):
+    """Per-row sampling inputs and the logit-row list the engine fills (as LlamaModel)."""
+    dev = model.dev
+    model.logit_rows = torch.zeros(R, dtype=torch.int32, device=dev)
+    model.temperature = torch.zeros(R, device=dev)
+    model.top_k = torch.zeros(R, dtype=torch.int32, device=dev)
+    model.top_p = torch.ones(R, device=dev)
+    model.uniforms = torch.zeros(R, device=dev)
+
+
+def compact_logit_rows(model, n_logits: int):
+    if n_logits > 0:
+        idx = model.logit_rows[:n_logits].long()
+        model.logits[:n_logits] = model.logits.index_select(0, idx)
+        model.next_ids[:n_logits] = model.next_ids.index_select(0, idx)
 
 
 class LatentCache:

@@ -198,6 +198,12 @@ class QwenNextModel:
         self.attn_counters = torch.zeros(R * nkv, dtype=torch.int32, device=dev)
         self._graphs = {}
         self.launches_per_graph = 0
+        from .deepseek import engine_buffers
+        engine_buffers(self, R)
+
+    row_limit = property(lambda self: self.max_rows)  # rows one forward takes (engine chunking)
+    # the DeltaNet recurrence is sequential: one forward may hold at most one row per sequence
+    serial_rows = True
 
     def reset_state(self, slot: int):
         self.conv_state[:, slot].zero_()
@@ -276,7 +282,14 @@ class QwenNextModel:
         mixed_gemv_swiglu(t, L.idx["sg"], L.idx["su"], xa, hs)
         mixed_gemv(t, L.idx["sd"], hs, self.x[:rows], residual=True, gate_logit=self.sglog[:rows])
 
-    def forward(self, rows: int, sample: str = "greedy", advance: bool = False):
+    def forward(self, rows: int, sample: str = "greedy", advance: bool = False, n_logits: int = 0):
+        """``n_logits`` (engine): > 0 moves the logits / greedy ids of ``logit_rows[:n_logits]`` to
+        the first rows. Rows must belong to distinct sequences (``serial_rows``)."""
+        from .deepseek import compact_logit_rows
+        self._forward(rows, sample, advance)
+        compact_logit_rows(self, n_logits)
+
+    def _forward(self, rows: int, sample: str = "greedy", advance: bool = False):
         cfg, w, inp = self.cfg, self.w, self.inp
         ops.embed(w.embed, inp.ids[:rows], self.x[:rows])
         for l, L in enumerate(w.layers):
@@ -318,11 +331,17 @@ class QwenNextModel:
         key = (rows, sample, advance)
         g = self._graphs.get(key)
         if g is None:
+            # the warm-up forward (lazy set-up outside the capture) advances the recurrent state:
+            # keep a copy and put it back, so the step's replay is its only update
+            saved = (self.conv_state.clone(), self.ssm_state.clone())
             s = torch.cuda.Stream(self.dev)
             s.wait_stream(torch.cuda.current_stream(self.dev))
             with torch.cuda.stream(s):
                 self.forward(rows, "none")
             torch.cuda.current_stream(self.dev).wait_stream(s)
+            self.conv_state.copy_(saved[0])
+            self.ssm_state.copy_(saved[1])
+            del saved
             g = torch.cuda.CUDAGraph()
             n0 = ops.launches.n
             with torch.cuda.graph(g):
