@@ -155,6 +155,23 @@ def write_llama_family_gguf(path: str, cfg: ModelConfig, seed: int = 0, std: flo
     return b.write(path)
 
 
+def write_tokenizer_gguf(path: str, vocab: int, arch: str = "llama") -> str:
+    """A GGUF file holding only the synthetic byte-level BPE tokenizer of ``vocab`` tokens (no
+    tensors): the tokenizer for models built from random weights without a GGUF of their own."""
+    toks, merges, bos, eos = synthetic_bpe_vocab(vocab)
+    b = GgufBuilder(arch)
+    b.set("general.name", "synthetic-tokenizer")
+    b.set("tokenizer.ggml.model", "gpt2")
+    b.set("tokenizer.ggml.pre", "llama-bpe")
+    b.set("tokenizer.ggml.tokens", toks)
+    b.set("tokenizer.ggml.merges", merges)
+    b.set("tokenizer.ggml.bos_token_id", bos, 4)
+    b.set("tokenizer.ggml.eos_token_id", eos, 4)
+    b.arch_set("vocab_size", vocab)
+    b.write(path)
+    return path
+
+
 def random_prompt(n: int, vocab: int, seed: int = 1) -> list:
     """Uniform-random token ids (the benchmark prompts)."""
     return np.random.default_rng(seed).integers(0, vocab, size=n).tolist()

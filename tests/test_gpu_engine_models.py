@@ -58,3 +58,27 @@ def test_engine_qwen_next_waves_match_model():
     assert [len(t) for t in two] == [4, 4]
     again = eng.generate([prompt], SamplingParams(max_tokens=5))[0]
     assert again == got  # the recurrent state was reset for the new sequence
+
+
+def test_serve_deepseek_preset_completion():
+    """The OpenAI server on the MLA + MoE engine (random weights, synthetic tokenizer)."""
+    import http.client
+    import json
+
+    from hawking_b200.serve import ServeLoop
+    from hawking_b200.serve.__main__ import preset_engine
+    eng, tok = preset_engine("deepseek-v3", layers=4, max_batch=2, max_ctx=512)
+    loop = ServeLoop(eng, tok, port=0, model_id="ds").start()
+    th = loop.run_in_thread()
+    try:
+        c = http.client.HTTPConnection("127.0.0.1", loop.port, timeout=300)
+        c.request("POST", "/v1/completions", body=json.dumps({"prompt": "hello world", "max_tokens": 5,
+                                                                "temperature": 0}))
+        r = c.getresponse()
+        body = r.read().decode()
+        assert r.status == 200, body
+        o = json.loads(body)
+        assert 1 <= o["usage"]["completion_tokens"] <= 5
+    finally:
+        loop.stop()
+        th.join(timeout=10)

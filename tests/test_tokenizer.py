@@ -120,3 +120,13 @@ def test_tokenizer_from_gguf(native, tmp_path):
     tok = native.Tokenizer.from_gguf(f)
     assert not tok.add_bos
     assert [tok.token(i) for i in tok.encode("Hello the world")] == ["Hello", "Ġthe", "Ġworld"]
+
+
+def test_tokenizer_only_gguf_roundtrip(tmp_path, native):
+    """The tensor-less synthetic tokenizer file (served with random-weight presets)."""
+    from hawking_b200.formats.synth import write_tokenizer_gguf
+    p = write_tokenizer_gguf(str(tmp_path / "tok.gguf"), 4096)
+    tok = native.Tokenizer.from_gguf(native.GgufFile.open(p))
+    ids = tok.encode("hello world, 123")
+    assert ids and max(ids) < 4096
+    assert tok.decode(ids) == "hello world, 123"
