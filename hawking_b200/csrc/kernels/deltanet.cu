@@ -12,7 +12,10 @@
 //      the output projection.
 // Kernel deltanet_conv: grid (key heads, rows). Kernel deltanet_recurrent: grid (value heads, rows),
 // 4 x dv threads; thread (quarter, column j) keeps rows [quarter * dk / 4, ...) of column j of S in
-// registers, so the state is read once and written once per token.
+// registers. Rows of one sequence may follow one another in a forward (a prompt chunk, in position
+// order): the CTA of a run's first row walks the whole run token by token, with the conv state and
+// the recurrent state S carried across tokens (S read once and written once per run); the CTAs of
+// the run's other rows return at once.
 //
 // Parity: crates/hawking-core/shaders/qwen80_device_activations.metal (causal conv update, q/k L2
 // + repeat :120-185, ba_to_decay_beta :187-206, gated rmsnorm :208-277, gated_delta_decode
@@ -22,15 +25,28 @@
 namespace hk {
 
 // ---- 1 + 2: conv + SiLU + L2 ------------------------------------------------------------------
+// The run of rows [r0, r1] that shares row r0's state slot, or r1 < r0 when row r0 continues a run.
+__device__ __forceinline__ int2 deltanet_run(const int* state_slot, int r0, int rows) {
+  if (!state_slot) return make_int2(r0, r0);
+  const int slot = state_slot[r0];
+  if (r0 > 0 && state_slot[r0 - 1] == slot) return make_int2(r0, r0 - 1);
+  int r1 = r0;
+  while (r1 + 1 < rows && state_slot[r1 + 1] == slot) ++r1;
+  return make_int2(r0, r1);
+}
+
 __global__ void __launch_bounds__(256) deltanet_conv_kernel(DeltaConvArgs a) {
   __shared__ float red[2][8];
   pdl_wait();
-  const int kh = blockIdx.x, r = blockIdx.y, tid = threadIdx.x;
+  const int kh = blockIdx.x, tid = threadIdx.x;
+  const int2 run = deltanet_run(a.state_slot, blockIdx.y, gridDim.y);
   const int dk = a.dk, rv = a.r * a.dv;  // value rows per key head
   const int key_elems = a.kh * dk;
   const int ch_total = 2 * key_elems + a.kh * rv;
-  const int slot = a.state_slot ? a.state_slot[r] : r;
+  const int slot = a.state_slot ? a.state_slot[run.x] : run.x;
   float* cst = a.conv_state + (int64_t)slot * ch_total * (a.kc - 1);
+  for (int r = run.x; r <= run.y; ++r) {
+  __syncthreads();  // the previous token's reduction scratch is free
   const float* in = a.qkvz + (int64_t)r * a.qkvz_stride + (int64_t)kh * (2 * dk + 2 * rv);
   auto conv = [&](int ch, float cur) {
     float* st = cst + (int64_t)ch * (a.kc - 1);
@@ -65,6 +81,7 @@ __global__ void __launch_bounds__(256) deltanet_conv_kernel(DeltaConvArgs a) {
       a.k[((int64_t)r * a.kh * a.r + vh) * dk + tid] = kv * ks;
     }
   }
+  }  // rows of the run
   pdl_launch();
 }
 
@@ -82,11 +99,18 @@ __global__ void __launch_bounds__(4 * DV) deltanet_recurrent_kernel(DeltaRecArgs
   __shared__ float red[32];
   __shared__ float s_decay, s_beta;
   pdl_wait();
-  const int vh = blockIdx.x, r = blockIdx.y, tid = threadIdx.x;
+  const int vh = blockIdx.x, tid = threadIdx.x;
+  const int2 run = deltanet_run(a.state_slot, blockIdx.y, gridDim.y);
+  if (run.y < run.x) { pdl_launch(); return; }  // another CTA walks this row's run
   const int j = tid % DV, qr = tid / DV;
   const int nvh = gridDim.x, kh = vh / a.r;
-  const int slot = a.state_slot ? a.state_slot[r] : r;
+  const int slot = a.state_slot ? a.state_slot[run.x] : run.x;
   float* S = a.state + ((int64_t)slot * nvh + vh) * DK * DV;
+  float s[QR];
+#pragma unroll
+  for (int i = 0; i < QR; ++i) s[i] = S[(int64_t)(qr * QR + i) * DV + j];
+  for (int r = run.x; r <= run.y; ++r) {
+  __syncthreads();  // the previous token's shared values are consumed
   for (int i = tid; i < DK; i += blockDim.x) {
     sk[i] = a.k[((int64_t)r * nvh + vh) * DK + i];
     sq[i] = a.q[((int64_t)r * nvh + vh) * DK + i];
@@ -101,11 +125,10 @@ __global__ void __launch_bounds__(4 * DV) deltanet_recurrent_kernel(DeltaRecArgs
   }
   __syncthreads();
   const float decay = s_decay, beta = s_beta;
-  float s[QR];
   float kvp = 0.f;
 #pragma unroll
   for (int i = 0; i < QR; ++i) {
-    s[i] = S[(int64_t)(qr * QR + i) * DV + j] * decay;
+    s[i] *= decay;
     kvp += s[i] * sk[qr * QR + i];
   }
   part[qr][j] = kvp;
@@ -116,13 +139,11 @@ __global__ void __launch_bounds__(4 * DV) deltanet_recurrent_kernel(DeltaRecArgs
 #pragma unroll
   for (int i = 0; i < QR; ++i) {
     s[i] += sk[qr * QR + i] * delta;
-    S[(int64_t)(qr * QR + i) * DV + j] = s[i];
     op += s[i] * sq[qr * QR + i];
   }
   __syncthreads();
   part[qr][j] = op;
   __syncthreads();
-  pdl_launch();
   if (qr == 0) {
     const float o = part[0][j] + part[1][j] + part[2][j] + part[3][j];
     // gated RMSNorm over the head's DV outputs (threads 0..DV-1 = whole warps)
@@ -146,6 +167,10 @@ __global__ void __launch_bounds__(4 * DV) deltanet_recurrent_kernel(DeltaRecArgs
       a.os[(int64_t)r * (width / 32) + (col >> 5)] = d * qsum;
     }
   }
+  }  // rows of the run
+#pragma unroll
+  for (int i = 0; i < QR; ++i) S[(int64_t)(qr * QR + i) * DV + j] = s[i];
+  pdl_launch();
 }
 
 void deltanet_recurrent_launch(const DeltaRecArgs& a, int n_value_heads, int rows, cudaStream_t s, bool pdl) {

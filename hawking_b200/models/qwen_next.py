@@ -202,8 +202,9 @@ class QwenNextModel:
         engine_buffers(self, R)
 
     row_limit = property(lambda self: self.max_rows)  # rows one forward takes (engine chunking)
-    # the DeltaNet recurrence is sequential: one forward may hold at most one row per sequence
-    serial_rows = True
+    # rows of one sequence may share a forward (consecutive, in position order): the DeltaNet
+    # kernels walk such a run token by token with the states carried across it
+    serial_rows = False
 
     def reset_state(self, slot: int):
         self.conv_state[:, slot].zero_()
@@ -308,8 +309,8 @@ class QwenNextModel:
             ops.advance(inp.ids, self.next_ids, inp.positions, inp.row_ctx, rows)
 
     def forward_tokens(self, tokens, seq_id: int = 0, start_pos: int = 0) -> torch.Tensor:
-        """Teacher-forced token-serial forward of one sequence (the recurrence is sequential);
-        returns fp32 logits [len(tokens), vocab]."""
+        """Teacher-forced forward of one sequence in chunks of up to ``max_rows`` tokens (the
+        DeltaNet kernels run each chunk's recurrence token by token); fp32 logits [n, vocab]."""
         kv = self.kv
         n = len(tokens)
         if not kv.bm.reserve(seq_id, start_pos + n):
@@ -319,12 +320,14 @@ class QwenNextModel:
         if start_pos == 0:
             self.reset_state(r)
         out = torch.empty(n, self.cfg.vocab, device=self.dev)
-        for i, t in enumerate(tokens):
-            p = start_pos + i
-            slot = kv.bm.slots(seq_id, p, p + 1)
-            self.inp.upload([int(t)], [p], slot, [r], [p + 1])
-            self.forward(1, "greedy")
-            out[i] = self.logits[0]
+        for c0 in range(0, n, self.max_rows):
+            c1 = min(n, c0 + self.max_rows)
+            p0 = start_pos + c0
+            slots = kv.bm.slots(seq_id, p0, start_pos + c1)
+            pos = list(range(p0, start_pos + c1))
+            self.inp.upload([int(t) for t in tokens[c0:c1]], pos, slots, [r] * (c1 - c0), [p + 1 for p in pos])
+            self.forward(c1 - c0, "greedy")
+            out[c0:c1] = self.logits[: c1 - c0]
         return out
 
     def graph_forward(self, rows: int, sample: str = "greedy", advance: bool = False):
