@@ -207,10 +207,89 @@ __global__ void __launch_bounds__(256) rope_append_kernel(RopeAppendArgs a) {
   pdl_launch();
 }
 
+// Head dim 128 with full-width rotation: every lane holds 4 consecutive elements of its head as
+// one float4 (loaded once, stored once), adjacent-pair rotation stays inside the lane and the neox
+// halves swap with the lane 16 apart; no shared-memory staging.
+__global__ void __launch_bounds__(256) rope_append_hd128_kernel(RopeAppendArgs a) {
+  pdl_wait();
+  const int r = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  const int pos = a.positions[r];
+  int64_t slot = -1;
+  if (a.slots) slot = a.slots[r];
+  else if (a.block_tables)
+    slot = (int64_t)a.block_tables[(int64_t)a.row_seq[r] * a.max_blocks + pos / a.block_size] * a.block_size +
+           pos % a.block_size;
+  const float* rope = a.rope + (int64_t)pos * 128;  // 64 (cos, sin) pairs
+  const int nheads = a.nh + 2 * a.nkv;
+  for (int h = blockIdx.x * nw + warp; h < nheads; h += gridDim.x * nw) {
+    const int kind = h < a.nh ? 0 : (h < a.nh + a.nkv ? 1 : 2);  // q, k, v
+    float4 v = reinterpret_cast<const float4*>(a.qkv + (int64_t)r * a.qkv_stride + (int64_t)h * 128)[lane];
+    if (a.bias) {
+      const float4 b = reinterpret_cast<const float4*>(a.bias + (int64_t)h * 128)[lane];
+      v.x += b.x; v.y += b.y; v.z += b.z; v.w += b.w;
+    }
+    const float* nw_ = kind == 0 ? a.q_norm : (kind == 1 ? a.k_norm : nullptr);
+    if (nw_) {
+      const float ss = warp_sum(v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w);
+      const float sc = rsqrtf(ss / 128.f + a.eps);
+      const float4 w = reinterpret_cast<const float4*>(nw_)[lane];
+      v.x *= sc * w.x; v.y *= sc * w.y; v.z *= sc * w.z; v.w *= sc * w.w;
+    }
+    if (kind < 2) {
+      if (a.rope_style == 0) {  // pairs (4l, 4l+1), (4l+2, 4l+3): rotation indices 2l, 2l+1
+        const float4 cs = reinterpret_cast<const float4*>(rope)[lane];
+        const float x0 = v.x, x1 = v.y, x2 = v.z, x3 = v.w;
+        v.x = x0 * cs.x - x1 * cs.y;
+        v.y = x0 * cs.y + x1 * cs.x;
+        v.z = x2 * cs.z - x3 * cs.w;
+        v.w = x2 * cs.w + x3 * cs.z;
+      } else {  // neox: element e < 64 pairs with e + 64 (lane ^ 16); rotation index e mod 64
+        float4 o;
+        o.x = __shfl_xor_sync(0xffffffffu, v.x, 16);
+        o.y = __shfl_xor_sync(0xffffffffu, v.y, 16);
+        o.z = __shfl_xor_sync(0xffffffffu, v.z, 16);
+        o.w = __shfl_xor_sync(0xffffffffu, v.w, 16);
+        const int p0 = (lane & 15) * 4;
+        const float4 c01 = reinterpret_cast<const float4*>(rope + 2 * p0)[0];  // c0 s0 c1 s1
+        const float4 c23 = reinterpret_cast<const float4*>(rope + 2 * p0)[1];  // c2 s2 c3 s3
+        if (lane < 16) {  // first half: x0 = mine, x1 = partner
+          v.x = v.x * c01.x - o.x * c01.y;
+          v.y = v.y * c01.z - o.y * c01.w;
+          v.z = v.z * c23.x - o.z * c23.y;
+          v.w = v.w * c23.z - o.w * c23.w;
+        } else {          // second half: x0 = partner, x1 = mine
+          v.x = o.x * c01.y + v.x * c01.x;
+          v.y = o.y * c01.w + v.y * c01.z;
+          v.z = o.z * c23.y + v.z * c23.x;
+          v.w = o.w * c23.w + v.w * c23.z;
+        }
+      }
+    }
+    if (kind == 0) {
+      reinterpret_cast<float4*>(a.q_out + ((int64_t)r * a.nh + h) * 128)[lane] = v;
+    } else if (slot >= 0) {
+      const int kh = kind == 1 ? h - a.nh : h - a.nh - a.nkv;
+      const int64_t blk = slot / a.block_size, off = slot % a.block_size;
+      __nv_bfloat16* cache = kind == 1 ? a.k_cache : a.v_cache;
+      const __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
+      uint2 pk;
+      pk.x = *reinterpret_cast<const uint32_t*>(&lo);
+      pk.y = *reinterpret_cast<const uint32_t*>(&hi);
+      reinterpret_cast<uint2*>(cache + ((blk * a.nkv + kh) * a.block_size + off) * 128)[lane] = pk;
+    }
+  }
+  pdl_launch();
+}
+
 void rope_append_launch(const RopeAppendArgs& a, cudaStream_t s, bool pdl) {
   if (a.hd % 32 || a.hd > 256) throw std::runtime_error("rope_append: head_dim must be a multiple of 32, <= 256");
   const int heads = a.nh + 2 * a.nkv;
-  launch(rope_append_kernel, dim3((heads + 7) / 8, a.R), dim3(256), 0, s, pdl, a);
+  const bool fast = a.hd == 128 && a.rot_dim == 128 && a.qkv_stride % 4 == 0 &&
+                    reinterpret_cast<uintptr_t>(a.qkv) % 16 == 0 && reinterpret_cast<uintptr_t>(a.bias) % 16 == 0 &&
+                    reinterpret_cast<uintptr_t>(a.q_norm) % 16 == 0 && reinterpret_cast<uintptr_t>(a.k_norm) % 16 == 0;
+  if (fast) launch(rope_append_hd128_kernel, dim3((heads + 7) / 8, a.R), dim3(256), 0, s, pdl, a);
+  else launch(rope_append_kernel, dim3((heads + 7) / 8, a.R), dim3(256), 0, s, pdl, a);
 }
 
 // ---- SwiGLU over a fused gate|up GEMM output ---------------------------------------------------

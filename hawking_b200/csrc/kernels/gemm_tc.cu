@@ -531,6 +531,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
           for (int e = 0; e < 8; ++e) {
             const int m = m0 + cj * 8 + e;
             if (m < a.M && n < a.N) {
+              // accumulate with fire-and-forget reductions: a load-add-store would put a load
+              // round trip per element on the epilogue (measured: prefill 43 -> 53 ms)
               float* dst = a.y + (int64_t)m * a.y_stride + n;
               if (a.atomic) atomicAdd(dst, v[e]);
               else *dst = v[e];

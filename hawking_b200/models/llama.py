@@ -337,7 +337,7 @@ class LlamaModel:
             if advance:
                 ops.advance(inp.ids, self.next_ids, inp.positions, inp.row_ctx, rows)
             return
-        if tc and w.lm_head.fmt == GgmlType.Q4_K:
+        if tc and w.lm_head.fmt == GgmlType.Q4_K and nl > GEMV_COLS:  # (a few sampled rows: the GEMV)
             ops.rmsnorm(x, w.out_norm, cfg.eps, yb=self.xb[:rows])
             src = self.xb[:rows]
             if n_logits:
@@ -459,15 +459,20 @@ class LlamaModel:
         x = self.x[:rows]
         ops.rmsnorm(x, lw.attn_norm, self.cfg.eps, yb=self.xb[:rows])
         qkv = self.qkv[:rows]
-        qkv.zero_()
+        once = ops.tc_gemm_overwrites(rows)  # persistent GEMM: plain stores, nothing to zero
+        if not once:
+            qkv.zero_()
         off = 0
         for wt in lw.wqkv:
-            ops.tc_gemm(wt, self.xb[:rows], qkv[:, off:off + wt.N], self.status, y_zeroed=True)
+            ops.tc_gemm(wt, self.xb[:rows], qkv[:, off:off + wt.N], self.status, y_zeroed=not once)
             off += wt.N
         self._rope_attention(l, lw, rows, splits, out_bf16=self.attb[:rows])
         if self.tp is not None:
-            self.partial[:rows].zero_()
-            ops.tc_gemm(lw.wo, self.attb[:rows], self.partial[:rows], self.status, atomic=True, y_zeroed=True)
+            if once:
+                ops.tc_gemm(lw.wo, self.attb[:rows], self.partial[:rows], self.status)
+            else:
+                self.partial[:rows].zero_()
+                ops.tc_gemm(lw.wo, self.attb[:rows], self.partial[:rows], self.status, atomic=True, y_zeroed=True)
             self._allreduce_partial_tc(rows)
         else:
             ops.tc_gemm(lw.wo, self.attb[:rows], x, self.status, atomic=True)
@@ -485,8 +490,12 @@ class LlamaModel:
             ops.tc_gemm(lw.w_gu, self.xb[:rows], gu, self.status, y_zeroed=True)
             ops.swiglu_bf16(gu, F, self.hb[:rows, :F], clear=True)
         if self.tp is not None:
-            self.partial[:rows].zero_()
-            ops.tc_gemm(lw.w_down, self.hb[:rows, :F], self.partial[:rows], self.status, atomic=True, y_zeroed=True)
+            if ops.tc_gemm_overwrites(rows):
+                ops.tc_gemm(lw.w_down, self.hb[:rows, :F], self.partial[:rows], self.status)
+            else:
+                self.partial[:rows].zero_()
+                ops.tc_gemm(lw.w_down, self.hb[:rows, :F], self.partial[:rows], self.status, atomic=True,
+                            y_zeroed=True)
             self._allreduce_partial_tc(rows)
         else:
             ops.tc_gemm(lw.w_down, self.hb[:rows, :F], x, self.status, atomic=True)

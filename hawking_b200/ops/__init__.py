@@ -224,6 +224,12 @@ def embed(table: QWeight, ids: torch.Tensor, out: torch.Tensor):
 PERSISTENT_GEMM = True
 
 
+def tc_gemm_overwrites(M: int) -> bool:
+    """Whether a tensor-core GEMM over M rows (engine tile choice) writes every output element
+    exactly once with a plain store (the persistent path: no split-K), so y needs no zeroing."""
+    return PERSISTENT_GEMM and M >= 192
+
+
 def tc_gemm(w: QWeight, x: torch.Tensor, y: torch.Tensor, status: torch.Tensor, atomic: bool = False,
             y_zeroed: bool = False, k_splits: int = 0, bn: int = 0):
     """y[M, N] (+)= x[M, K] (bf16) @ w[N, K]^T on the tensor cores (Q4_K weights).

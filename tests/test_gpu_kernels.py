@@ -115,6 +115,33 @@ def test_rope_append(style, hd):
                                    qkv[r, (nh + nkv) * hd:].view(nkv, hd).bfloat16().float())
 
 
+@pytest.mark.parametrize("style", [0, 1])
+def test_rope_append_bias_and_head_norms(style):
+    """Qwen-style projection bias and per-head RMSNorm of q / k before the rotation (hd 128)."""
+    nh, nkv, R, bs, hd = 4, 2, 2, 16, 128
+    g = torch.Generator(device=DEV).manual_seed(style)
+    qkv = torch.randn(R, (nh + 2 * nkv) * hd, device=DEV, generator=g)
+    bias = torch.randn((nh + 2 * nkv) * hd, device=DEV, generator=g) * 0.1
+    qn, kn = torch.rand(hd, device=DEV, generator=g) + 0.5, torch.rand(hd, device=DEV, generator=g) + 0.5
+    pos = torch.tensor([3, 9], dtype=torch.int32, device=DEV)
+    slots = torch.tensor([1, 20], dtype=torch.int32, device=DEV)
+    rope = ops.rope_table(64, hd, 10000.0, device=DEV)
+    q = torch.zeros(R, nh, hd, device=DEV)
+    kc = torch.zeros(2, nkv, bs, hd, dtype=torch.bfloat16, device=DEV)
+    vc = torch.zeros_like(kc)
+    ops.rope_append(qkv, pos, slots, rope, hd, style, q, kc, vc, nh, nkv, hd, bs, bias=bias, q_norm=qn, k_norm=kn,
+                    eps=1e-6)
+    x = qkv + bias
+
+    def norm(t, w):
+        return t * torch.rsqrt((t * t).mean(-1, keepdim=True) + 1e-6) * w
+    qr = rope_ref(norm(x[:, : nh * hd].view(R, nh, hd), qn), pos.long(), 10000.0, hd, style)
+    kr = rope_ref(norm(x[:, nh * hd:(nh + nkv) * hd].view(R, nkv, hd), kn), pos.long(), 10000.0, hd, style)
+    torch.testing.assert_close(q, qr, rtol=1e-4, atol=1e-4)
+    for r, s_ in enumerate(slots.tolist()):
+        torch.testing.assert_close(kc[s_ // bs, :, s_ % bs].float(), kr[r], rtol=2 ** -7, atol=1e-4)
+
+
 def _paged_attention_ref(q, kc, vc, tables, row_seq, row_ctx, scale):
     R, nh, hd = q.shape
     nkv, bs = kc.shape[1], kc.shape[2]
