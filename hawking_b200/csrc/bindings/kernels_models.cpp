@@ -349,7 +349,8 @@ void mla_decode(const Tensor& q_lat, const Tensor& q_pe, const Tensor& cache, co
   a.o_lat = ptr<float>(o_lat);
   a.status = ptr<int>(status);
   const c10::cuda::CUDAGuard g(q_lat.device());
-  hk::mla_decode_launch(a, cur_stream(), pdl);
+  if (num_splits <= 0) hk::mla_flash_decode_launch(a, cur_stream(), pdl);  // tensor-core kernel
+  else hk::mla_decode_launch(a, cur_stream(), pdl);
 }
 
 void mla_out(const Tensor& o_lat, const Tensor& w_uv, const Tensor& oq, const Tensor& od, const Tensor& os, bool pdl) {

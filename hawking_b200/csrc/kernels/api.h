@@ -510,6 +510,9 @@ struct MlaDecodeArgs {
 };
 int mla_heads_per_cta(int nh, int rows);  // heads sharing one CTA in mla_decode
 void mla_decode_launch(MlaDecodeArgs a, cudaStream_t s, bool pdl);
+// Tensor-core variant (mla_flash.cu): 16 heads per CTA on mma.sync, splits and output slices chosen
+// to cover the GPU (num_splits / stage_blocks ignored).
+void mla_flash_decode_launch(const MlaDecodeArgs& a, cudaStream_t s, bool pdl);
 struct MlaOutArgs {
   const float* o_lat;
   const __nv_bfloat16* w_uv;  // [nh, vdim, 512]

@@ -67,7 +67,7 @@ def build_cases(dev: str = "cuda", ctx: int = 2048, rows: int = 1, only=None, bn
     cases = {}
     if only is not None and all(c.startswith("tc_") or c == "attention_prefill" for c in only):
         return _tc_cases(dev, ctx, rows, g, only, bn)
-    if only is not None and all(c.startswith("mla_decode") for c in only):
+    if only is not None and all(c.startswith("mla_") for c in only):
         return _mla_cases(dev, ctx, rows, g)
     wo, wd, wqkv, wgu = copies((H, H)), copies((H, F)), copies((6144, H)), copies((F, H), (F, H))
     x = torch.randn(rows, H, device=dev)
@@ -139,6 +139,9 @@ def _mla_cases(dev, ctx, rows, g):
         splits = 1
         while splits < 8 and rows * groups * splits < 148:
             splits *= 2
+        cases[f"mla_flash_h{nh}"] = (
+            lambda i, ql=ql, qp=qp, o=o: K.mla_decode(ql, qp, cache, tables, rs, rc, 0.07, 0, o, st, True),
+            rows * ctx * 576 * 2, 2.0 * rows * ctx * nh * (576 + 512))
         cases[f"mla_decode_h{nh}"] = (
             lambda i, ql=ql, qp=qp, o=o, splits=splits: K.mla_decode(ql, qp, cache, tables, rs, rc, 0.07, splits, o, st,
                                                                      True),
