@@ -5,7 +5,9 @@
 #include "../native/gguf.h"
 #include "../native/http_server.h"
 #include "../native/json.h"
+#include "../native/json_constrain.h"
 #include "../native/tokenizer.h"
+#include "../native/tool_calls.h"
 
 namespace py = pybind11;
 using namespace hk;
@@ -64,7 +66,10 @@ void bind_serve(py::module_& m) {
       .def_readwrite("max_connections", &ServeOptions::max_connections)
       .def_readwrite("default_max_tokens", &ServeOptions::default_max_tokens)
       .def_readwrite("max_context", &ServeOptions::max_context)
-      .def_readwrite("request_timeout_s", &ServeOptions::request_timeout_s);
+      .def_readwrite("request_timeout_s", &ServeOptions::request_timeout_s)
+      .def_readwrite("max_batch", &ServeOptions::max_batch)
+      .def_readwrite("architecture", &ServeOptions::architecture)
+      .def_readwrite("recurrent_state_bytes", &ServeOptions::recurrent_state_bytes);
 
   py::class_<ServeRequest>(m, "ServeRequest")
       .def_readonly("id", &ServeRequest::id)
@@ -78,7 +83,36 @@ void bind_serve(py::module_& m) {
       .def_readonly("repetition_penalty", &ServeRequest::repetition_penalty)
       .def_readonly("seed", &ServeRequest::seed)
       .def_readonly("stream", &ServeRequest::stream)
+      .def_readonly("json_mode", &ServeRequest::json_mode)
       .def_readonly("stop_ids", &ServeRequest::stop_ids);
+
+  py::class_<JsonConstraint>(m, "JsonConstraint")
+      .def(py::init<>())
+      .def("accepts", [](const JsonConstraint& c, const py::bytes& b) { return c.accepts(std::string(b)); })
+      .def("advance", [](JsonConstraint& c, const py::bytes& b) { return c.advance(std::string(b)); })
+      .def_property_readonly("done", &JsonConstraint::done)
+      .def("pick", [](const JsonConstraint& c, const Tokenizer& tok, py::buffer logits) {
+        py::buffer_info bi = logits.request();
+        if (bi.format != py::format_descriptor<float>::format() || bi.ndim != 1)
+          throw std::runtime_error("pick: 1-D float32 logits");
+        return c.pick(tok, static_cast<const float*>(bi.ptr), (int64_t)bi.shape[0]);
+      })
+      .def("mask", [](const JsonConstraint& c, const Tokenizer& tok, py::buffer logits) {
+        py::buffer_info bi = logits.request(true);
+        if (bi.format != py::format_descriptor<float>::format() || bi.ndim != 1)
+          throw std::runtime_error("mask: 1-D float32 logits");
+        c.mask(tok, static_cast<float*>(bi.ptr), (int64_t)bi.shape[0]);
+      })
+      .def_static("validate", &JsonConstraint::validate);
+
+  m.def("render_tools_preamble", [](const std::string& tools_json) {
+    return render_tools_preamble(Json::parse(tools_json));
+  });
+  m.def("extract_tool_calls", [](const std::string& text, const std::vector<std::string>& known) {
+    py::list out;
+    for (const auto& c : extract_tool_calls(text, known)) out.append(py::make_tuple(c.id, c.name, c.arguments));
+    return out;
+  }, py::arg("text"), py::arg("known_tools"));
 
   py::class_<HttpServer, std::shared_ptr<HttpServer>>(m, "HttpServer")
       .def(py::init<ServeOptions, std::shared_ptr<Tokenizer>>(), py::arg("options"), py::arg("tokenizer"))

@@ -1,5 +1,6 @@
 // OpenAI-compatible HTTP/1.1 + SSE server; see http_server.h.
 #include "http_server.h"
+#include "tool_calls.h"
 
 #include <arpa/inet.h>
 #include <netinet/in.h>
@@ -283,8 +284,55 @@ bool HttpServer::handle(int fd, const std::string& method, const std::string& pa
                               "not_implemented"),
                    keep_alive);
   }
+  if (path == "/v1/hawking/context") {
+    Json c = Json::object();
+    size_t active = 0;
+    {
+      std::lock_guard<std::mutex> g(mu_);
+      active = pending_.size();
+    }
+    c.set("model_id", Json::string(opts_.model_id));
+    c.set("arch", Json::string(opts_.architecture));
+    c.set("ctx_len_native", Json::integer(opts_.max_context));
+    c.set("ctx_len_effective", Json::integer(opts_.max_context));
+    c.set("tq_multiplier", Json::number(1.0));
+    c.set("tq_estimated", Json::boolean(false));
+    c.set("recurrent_state_bytes",
+          opts_.recurrent_state_bytes > 0 ? Json::integer(opts_.recurrent_state_bytes) : Json::null());
+    c.set("active_slots", Json::integer((int64_t)active));
+    c.set("free_slots", Json::integer(std::max<int64_t>(0, (int64_t)opts_.max_batch - (int64_t)active)));
+    c.set("max_batch", Json::integer(opts_.max_batch));
+    return respond(fd, 200, "application/json", c.dump(), keep_alive);
+  }
+  if (path == "/v1/hawking/surface") {
+    Json o = Json::object();
+    o.set("server", Json::string("hawking-b200"));
+    Json routes = Json::array();
+    for (const char* r : {"GET /healthz", "GET /metrics", "GET /v1/models", "POST /v1/chat/completions",
+                          "POST /v1/completions", "POST /v1/embeddings", "POST /v1/hawking/generate",
+                          "POST /v1/hawking/tokens", "GET /v1/hawking/context", "GET /v1/hawking/surface"})
+      routes.push(Json::string(r));
+    o.set("routes", routes);
+    Json ni = Json::array();
+    ni.push(Json::string("POST /v1/responses"));
+    ni.push(Json::string("POST /v1/messages"));
+    o.set("not_implemented", ni);
+    Json f = Json::object();
+    for (const char* k : {"streaming", "tool_calls", "json_mode", "embeddings", "continuous_batching",
+                          "prefix_reuse", "speculative_decoding"})
+      f.set(k, Json::boolean(true));
+    o.set("features", f);
+    Json fam = Json::object();
+    for (const char* a : {"llama", "qwen2", "qwen3", "mixtral", "qwen2moe", "qwen3moe", "qwen3next", "deepseek2"})
+      fam.set(a, Json::string("served"));
+    o.set("architectures", fam);
+    o.set("model_id", Json::string(opts_.model_id));
+    o.set("arch", Json::string(opts_.architecture));
+    return respond(fd, 200, "application/json", o.dump(), keep_alive);
+  }
   const bool chat = path == "/v1/chat/completions", comp = path == "/v1/completions", emb = path == "/v1/embeddings";
-  if (!chat && !comp && !emb) return respond_error(fd, 404, "no route for " + path, "not_found", keep_alive);
+  const bool hgen = path == "/v1/hawking/generate", htok = path == "/v1/hawking/tokens";
+  if (!chat && !comp && !emb && !hgen && !htok) return respond_error(fd, 404, "no route for " + path, "not_found", keep_alive);
   if (method != "POST") return respond_error(fd, 405, "use POST", "method_not_allowed", keep_alive);
   Json j;
   try {
@@ -295,6 +343,11 @@ bool HttpServer::handle(int fd, const std::string& method, const std::string& pa
   }
   if (!j.is_object()) return respond_error(fd, 400, "request body must be a JSON object", "invalid_json", keep_alive);
   if (emb) return handle_embeddings(fd, j, keep_alive);
+  if (hgen || htok) {
+    if (!j["prompt"].is_string() || j["prompt"].as_string().empty())
+      return respond_error(fd, 400, "'prompt' must not be empty", "missing_required_parameter", keep_alive);
+    return handle_generate(fd, j, false, keep_alive, hgen ? "generate" : "tokens");
+  }
   return handle_generate(fd, j, chat, keep_alive);
 }
 
@@ -308,8 +361,19 @@ std::string HttpServer::resolve_template() const {
 std::string HttpServer::render_chat(const Json& messages, const std::string& tmpl) const {
   std::string out;
   for (const auto& m : messages.items()) {
-    const std::string role = m["role"].is_string() ? m["role"].as_string() : "user";
-    const std::string text = content_text(m["content"]);
+    std::string role = m["role"].is_string() ? m["role"].as_string() : "user";
+    std::string text = content_text(m["content"]);
+    if (role == "tool") {  // a tool result goes back to the model as a user turn
+      role = "user";
+      text = "<tool_response>\n" + text + "\n</tool_response>";
+    }
+    if (m["tool_calls"].is_array())  // the assistant's earlier calls, in the format it was taught
+      for (const auto& tc : m["tool_calls"].items()) {
+        const Json& f = tc["function"];
+        std::string args = f["arguments"].is_string() ? f["arguments"].as_string() : f["arguments"].dump();
+        text += "<tool_call>\n{\"name\": " + Json::string(f["name"].is_string() ? f["name"].as_string() : "").dump() +
+                ", \"arguments\": " + args + "}\n</tool_call>";
+      }
     if (tmpl == "llama3") out += "<|start_header_id|>" + role + "<|end_header_id|>\n\n" + text + "<|eot_id|>";
     else if (tmpl == "chatml") out += "<|im_start|>" + role + "\n" + text + "<|im_end|>\n";
     else if (tmpl == "deepseek") {
@@ -345,15 +409,45 @@ void HttpServer::forget(uint64_t id) {
   pending_.erase(id);
 }
 
-bool HttpServer::handle_generate(int fd, const Json& j, bool chat, bool keep_alive) {
+bool HttpServer::handle_generate(int fd, const Json& j, bool chat, bool keep_alive, const std::string& native) {
   ServeRequest r;
   r.kind = chat ? "chat" : "completion";
   std::string prompt_text;
+  std::vector<std::string> known_tools;
+  const bool tools_on = chat && j["tools"].is_array() && j["tools"].size() > 0 &&
+                        !(j["tool_choice"].is_string() && j["tool_choice"].as_string() == "none");
   if (chat) {
     if (!j["messages"].is_array()) return respond_error(fd, 400, "'messages' must be an array", "invalid_json", keep_alive);
     if (j["messages"].size() == 0)
       return respond_error(fd, 400, "'messages' must not be empty", "missing_required_parameter", keep_alive);
-    prompt_text = render_chat(j["messages"], resolve_template());
+    if (tools_on) {  // the tools preamble leads the system turn
+      known_tools = tool_names(j["tools"]);
+      Json msgs = Json::array();
+      const std::string pre = render_tools_preamble(j["tools"]);
+      bool merged = false;
+      for (const auto& m : j["messages"].items()) {
+        if (!merged && m["role"].is_string() && m["role"].as_string() == "system") {
+          Json sys = Json::object();
+          sys.set("role", Json::string("system"));
+          sys.set("content", Json::string(content_text(m["content"]) + "\n\n" + pre));
+          msgs.push(sys);
+          merged = true;
+        } else {
+          msgs.push(m);
+        }
+      }
+      if (!merged) {
+        Json all = Json::array(), sys = Json::object();
+        sys.set("role", Json::string("system"));
+        sys.set("content", Json::string(pre));
+        all.push(sys);
+        for (const auto& m : msgs.items()) all.push(m);
+        msgs = all;
+      }
+      prompt_text = render_chat(msgs, resolve_template());
+    } else {
+      prompt_text = render_chat(j["messages"], resolve_template());
+    }
   } else {
     const Json& p = j["prompt"];
     if (p.is_string()) prompt_text = p.as_string();
@@ -375,12 +469,15 @@ bool HttpServer::handle_generate(int fd, const Json& j, bool chat, bool keep_ali
     r.max_tokens = std::max(1, opts_.max_context - (int)r.prompt.size());
   if ((int)r.prompt.size() >= opts_.max_context)
     return respond_error(fd, 400, "prompt longer than the context window", "context_length_exceeded", keep_alive);
-  r.temperature = (float)num_or(j, "temperature", 1.0);
-  r.top_p = (float)num_or(j, "top_p", 1.0);
-  r.top_k = (int)num_or(j, "top_k", 0);
+  r.temperature = (float)num_or(j, "temperature", native.empty() ? 1.0 : 0.0);
+  r.top_p = (float)num_or(j, "top_p", native == "generate" && r.temperature > 0.f ? 0.9 : 1.0);
+  r.top_k = (int)num_or(j, "top_k", native == "generate" && r.temperature > 0.f ? 40 : 0);
+  if (native == "tokens") r.temperature = 0.f;  // greedy token stream
+  r.json_mode = j["response_format"].is_object() && j["response_format"]["type"].is_string() &&
+                j["response_format"]["type"].as_string() == "json_object";
   r.repetition_penalty = (float)num_or(j, "repetition_penalty", 1.0);
   r.seed = (uint64_t)num_or(j, "seed", 42);
-  r.stream = j["stream"].type() == Json::Type::Bool && j["stream"].as_bool();
+  r.stream = native == "tokens" || (native.empty() && j["stream"].type() == Json::Type::Bool && j["stream"].as_bool());
   r.stop_ids = tok_->eog_ids();
   std::vector<std::string> stops;
   if (j["stop"].is_string()) stops.push_back(j["stop"].as_string());
@@ -432,6 +529,8 @@ bool HttpServer::handle_generate(int fd, const Json& j, bool chat, bool keep_ali
         "HTTP/1.1 200 OK\r\nContent-Type: text/event-stream\r\nCache-Control: no-cache\r\nConnection: close\r\n\r\n";
     if (!write_all(fd, h)) client_gone = true;
   }
+  const auto t_start = Clock::now();
+  auto t_first = t_start;
   bool first = true;
   const auto deadline = Clock::now() + std::chrono::milliseconds((int64_t)(opts_.request_timeout_s * 1000));
   while (!client_gone) {
@@ -467,8 +566,14 @@ bool HttpServer::handle_generate(int fd, const Json& j, bool chat, bool keep_ali
       return respond_error(fd, 504, "generation timed out", "timeout", keep_alive);
     }
     for (int32_t t : toks) {
+      if (n_gen == 0) t_first = Clock::now();
       n_gen++;
       tokens_generated_++;
+      if (native == "tokens" && !client_gone) {  // token ids as they come
+        Json e = Json::object();
+        e.set("token", Json::integer(t));
+        if (!write_all(fd, "data: " + e.dump() + "\n\n")) client_gone = true;
+      }
       if (tok_->is_eog(t)) continue;
       text += dec.push(t);
     }
@@ -486,6 +591,11 @@ bool HttpServer::handle_generate(int fd, const Json& j, bool chat, bool keep_ali
       fin = 2;
     }
     if (done) finish_reason = fin == 1 ? "length" : "stop";
+    if (native == "tokens") {
+      if (done && !client_gone) write_all(fd, "data: [DONE]\n\n");
+      if (done) break;
+      continue;
+    }
     if (stream) {
       const size_t hold = done ? 0 : stop_holdback(text, stops);
       const size_t upto = text.size() - std::min(hold, text.size() - sent);
@@ -496,7 +606,34 @@ bool HttpServer::handle_generate(int fd, const Json& j, bool chat, bool keep_ali
         sent = upto;
       }
       if (done && !client_gone) {
-        write_all(fd, chunk_json("", finish_reason, false));
+        const auto calls = tools_on ? extract_tool_calls(text, known_tools) : std::vector<ToolCall>{};
+        if (!calls.empty()) {  // the calls as one final delta
+          Json c = Json::object();
+          c.set("id", Json::string(oid));
+          c.set("object", Json::string("chat.completion.chunk"));
+          c.set("created", Json::integer(created));
+          c.set("model", Json::string(opts_.model_id));
+          Json ch = Json::object(), d = Json::object(), arr = Json::array(), tcs = Json::array();
+          for (size_t i = 0; i < calls.size(); ++i) {
+            Json tc = Json::object(), f = Json::object();
+            tc.set("index", Json::integer((int64_t)i));
+            tc.set("id", Json::string(calls[i].id));
+            tc.set("type", Json::string("function"));
+            f.set("name", Json::string(calls[i].name));
+            f.set("arguments", Json::string(calls[i].arguments));
+            tc.set("function", f);
+            tcs.push(tc);
+          }
+          d.set("tool_calls", tcs);
+          ch.set("index", Json::integer(0));
+          ch.set("delta", d);
+          ch.set("finish_reason", Json::string("tool_calls"));
+          arr.push(ch);
+          c.set("choices", arr);
+          write_all(fd, "data: " + c.dump() + "\n\n");
+        } else {
+          write_all(fd, chunk_json("", finish_reason, false));
+        }
         write_all(fd, "data: [DONE]\n\n");
       }
     }
@@ -509,6 +646,21 @@ bool HttpServer::handle_generate(int fd, const Json& j, bool chat, bool keep_ali
   }
   requests_finished_++;
   if (stream || client_gone) return false;
+  if (native == "generate") {
+    const double total_ms = std::chrono::duration<double, std::milli>(Clock::now() - t_start).count();
+    const double decode_ms = std::chrono::duration<double, std::milli>(Clock::now() - t_first).count();
+    Json st = Json::object();
+    st.set("prompt_tokens", Json::integer((int64_t)n_prompt));
+    st.set("completion_tokens", Json::integer((int64_t)n_gen));
+    st.set("decode_ms", Json::number(decode_ms));
+    st.set("dec_tps", Json::number(n_gen > 1 ? (double)(n_gen - 1) / std::max(decode_ms / 1000.0, 1e-6) : 0.0));
+    st.set("ttft_ms", Json::number(total_ms - decode_ms));
+    Json o = Json::object();
+    o.set("text", Json::string(text));
+    o.set("finish_reason", Json::string(finish_reason));
+    o.set("stats", st);
+    return respond(fd, 200, "application/json", o.dump(), keep_alive);
+  }
   Json o = Json::object();
   o.set("id", Json::string(oid));
   o.set("object", Json::string(chat ? "chat.completion" : "text_completion"));
@@ -519,7 +671,24 @@ bool HttpServer::handle_generate(int fd, const Json& j, bool chat, bool keep_ali
   if (chat) {
     Json msg = Json::object();
     msg.set("role", Json::string("assistant"));
-    msg.set("content", Json::string(text));
+    const auto calls = tools_on ? extract_tool_calls(text, known_tools) : std::vector<ToolCall>{};
+    if (!calls.empty()) {
+      Json tcs = Json::array();
+      for (const auto& c : calls) {
+        Json tc = Json::object(), f = Json::object();
+        tc.set("id", Json::string(c.id));
+        tc.set("type", Json::string("function"));
+        f.set("name", Json::string(c.name));
+        f.set("arguments", Json::string(c.arguments));
+        tc.set("function", f);
+        tcs.push(tc);
+      }
+      msg.set("content", Json::null());
+      msg.set("tool_calls", tcs);
+      finish_reason = "tool_calls";
+    } else {
+      msg.set("content", Json::string(text));
+    }
     ch.set("message", msg);
   } else {
     ch.set("text", Json::string(text));

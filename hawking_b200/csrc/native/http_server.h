@@ -10,11 +10,18 @@
 // Routes: GET /healthz, GET /metrics (Prometheus text), GET /v1/models,
 // POST /v1/chat/completions, POST /v1/completions (both with "stream": true -> SSE ending in
 // "data: [DONE]"), POST /v1/embeddings, and 501 bodies for POST /v1/responses and /v1/messages.
+// Chat requests with "tools" get the tools preamble in the prompt and their completion parsed for
+// tool calls (message.tool_calls, finish_reason "tool_calls"); "response_format":
+// {"type": "json_object"} marks the request JSON-constrained (the engine masks its sampling).
+// Native routes: POST /v1/hawking/generate (lean generate with decode statistics),
+// POST /v1/hawking/tokens (greedy token ids as SSE), GET /v1/hawking/context (context and slot
+// status), GET /v1/hawking/surface (routes, features and model families served).
 // Errors use the OpenAI shape {"error": {"message", "type", "code"}}.
 //
 // Parity: crates/hawking-serve/src/http.rs:265-281 (routes), :307 (healthz), :329-365 (metrics
 // names), :610 / :673 (chat / completions), :828 (SSE [DONE]), :1410 (embeddings), :290-305
-// (501 stubs), :43-91 (error body), :871 (wait queue bounded at max_batch * 8).
+// (501 stubs), :43-91 (error body), :871 (wait queue bounded at max_batch * 8), :272-276 and
+// :971-1140 (/v1/hawking routes), :389-420 (context status), :650 (json_mode from response_format).
 #pragma once
 #include <atomic>
 #include <condition_variable>
@@ -42,6 +49,9 @@ struct ServeOptions {
   int default_max_tokens = 256;
   int max_context = 8192;
   double request_timeout_s = 600.0;
+  int max_batch = 8;               // engine decode slots (reported by /v1/hawking/context)
+  std::string architecture = "llama";
+  int64_t recurrent_state_bytes = 0;  // per sequence (hybrid models)
 };
 
 // One admitted request, handed to the engine loop by poll().
@@ -55,6 +65,7 @@ struct ServeRequest {
   int top_k = 0;
   uint64_t seed = 42;
   bool stream = false;
+  bool json_mode = false;         // constrain sampling to a JSON object
   std::vector<int32_t> stop_ids;  // end-of-generation token ids
 };
 
@@ -86,7 +97,8 @@ class HttpServer {
   void accept_loop();
   void serve_connection(int fd);
   bool handle(int fd, const std::string& method, const std::string& path, const std::string& body, bool keep_alive);
-  bool handle_generate(int fd, const Json& body, bool chat, bool keep_alive);
+  // native: "" (OpenAI shape), "generate" (/v1/hawking/generate), "tokens" (/v1/hawking/tokens)
+  bool handle_generate(int fd, const Json& body, bool chat, bool keep_alive, const std::string& native = "");
   bool handle_embeddings(int fd, const Json& body, bool keep_alive);
   std::string metrics_text() const;
   std::shared_ptr<Pending> admit(ServeRequest req);

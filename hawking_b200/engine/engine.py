@@ -36,6 +36,7 @@ class RequestState:
     t_arrival: float = 0.0
     t_first: Optional[float] = None
     t_done: Optional[float] = None
+    json: Optional[object] = None  # JsonConstraint of a JSON-mode request
 
 
 @dataclass
@@ -61,6 +62,7 @@ class Engine:
         self.use_graphs = use_graphs
         self.stats = EngineStats()
         self._host_ids = torch.zeros(model.max_rows, dtype=torch.int32).pin_memory()
+        self.tokenizer = None  # token bytes for JSON-mode requests (set by the server)
 
     # ---- construction helpers ----
     @staticmethod
@@ -141,7 +143,12 @@ class Engine:
         rid = next(self._ids)
         self.sched.add(rid, list(map(int, prompt)), params.max_tokens, params.greedy, list(params.stop_ids),
                        self.cfg.max_ctx)
-        self.requests[rid] = RequestState(rid, params, RequestRng(params.seed), t_arrival=time.perf_counter())
+        st = RequestState(rid, params, RequestRng(params.seed), t_arrival=time.perf_counter())
+        if params.json_mode:
+            if self.tokenizer is None:
+                raise ValueError("JSON mode needs the engine's tokenizer (Engine.tokenizer)")
+            st.json = native().JsonConstraint()
+        self.requests[rid] = st
         return rid
 
     def abort(self, rid: int):
@@ -275,6 +282,9 @@ class Engine:
         for it, r in rows_here:
             st = self.requests[it.id]
             p = st.params
+            if st.json is not None:
+                out.append(self._sample_json(st, m.logits[r]))
+                continue
             if p.temperature <= 0.0 and p.repetition_penalty == 1.0:
                 torch.cuda.current_stream(m.dev).synchronize()
                 out.append(int(torch.argmax(m.logits[r]).item()))
@@ -299,6 +309,42 @@ class Engine:
             out.append(int(m.next_ids[r].item()))
             self.stats.d2h_bytes += 4
         return out
+
+    def _sample_json(self, st: RequestState, logits: torch.Tensor) -> int:
+        """JSON mode: the best allowed token (greedy) or a draw from the allowed tokens; the
+        constraint then advances by the token's bytes. With no allowed token left, end of
+        generation."""
+        p = st.params
+        v = logits.float().cpu().numpy().copy()
+        self.stats.d2h_bytes += v.nbytes
+        tok = self.tokenizer
+        if p.temperature <= 0.0:
+            t = st.json.pick(tok, v)
+        else:
+            import numpy as np
+            st.json.mask(tok, v)
+            z = v / p.temperature
+            z -= np.max(z)
+            pr = np.exp(z)
+            if p.top_k > 0:
+                pr[np.argsort(-pr)[p.top_k:]] = 0.0
+            if pr.sum() <= 0 or not np.isfinite(pr.sum()):
+                t = -1
+            else:
+                pr /= pr.sum()
+                order = np.argsort(-pr)
+                keep = np.cumsum(pr[order]) - pr[order] < p.top_p
+                pr2 = np.zeros_like(pr)
+                pr2[order[keep]] = pr[order[keep]]
+                pr2 /= pr2.sum()
+                t = int(np.searchsorted(np.cumsum(pr2), st.rng.uniform(), side="right"))
+                t = min(t, len(pr2) - 1)
+        if t < 0:
+            eog = tok.eog_ids()
+            return int(eog[0]) if eog else 0
+        if not tok.is_eog(t):
+            st.json.advance(tok.token_bytes(t))
+        return int(t)
 
     def embed(self, ids: List[int]) -> List[float]:
         """L2-normalised final-position logits of a teacher-forced forward of ``ids`` on a scratch

@@ -22,10 +22,12 @@ class SamplingParams:
     seed: int = 42
     max_tokens: int = 16
     stop_ids: List[int] = field(default_factory=list)
+    json_mode: bool = False  # only tokens that keep the output a prefix of one JSON object
 
     @property
     def greedy(self) -> bool:
-        return self.temperature <= 0.0 and self.repetition_penalty == 1.0
+        """Served by the fused on-device argmax lane (JSON mode needs the logits on the host)."""
+        return self.temperature <= 0.0 and self.repetition_penalty == 1.0 and not self.json_mode
 
 
 class RequestRng:

@@ -30,8 +30,18 @@ class ServeLoop:
         o.max_queue = int(max_queue or 8 * getattr(engine, "max_batch", 64))
         o.default_max_tokens = default_max_tokens
         o.request_timeout_s = request_timeout_s
+        o.max_batch = int(getattr(engine, "max_batch", 8))
+        cfg = getattr(engine, "cfg", None)
+        o.architecture = str(getattr(cfg, "arch", "llama"))
+        model = getattr(engine, "model", None)
+        if model is not None and hasattr(model, "ssm_state"):  # recurrent state per sequence
+            per = model.ssm_state[:, 0].numel() * model.ssm_state.element_size() + \
+                model.conv_state[:, 0].numel() * model.conv_state.element_size()
+            o.recurrent_state_bytes = int(per)
         self.engine = engine
         self.tokenizer = tokenizer
+        if hasattr(engine, "tokenizer"):
+            engine.tokenizer = tokenizer  # JSON-mode requests mask tokens by their bytes
         self.server = native().HttpServer(o, tokenizer)
         self._to_server: Dict[int, int] = {}    # engine request id -> server request id
         self._to_engine: Dict[int, int] = {}
@@ -62,7 +72,7 @@ class ServeLoop:
                 continue
             p = SamplingParams(temperature=r.temperature, top_k=r.top_k, top_p=r.top_p,
                                repetition_penalty=r.repetition_penalty, seed=r.seed, max_tokens=r.max_tokens,
-                               stop_ids=list(r.stop_ids))
+                               stop_ids=list(r.stop_ids), json_mode=bool(r.json_mode))
             try:
                 erid = self.engine.add_request(list(r.prompt), p)
             except Exception as e:  # noqa: BLE001

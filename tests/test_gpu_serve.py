@@ -66,3 +66,16 @@ def test_chat_stream_and_embeddings(served):
     assert len(vecs) == 2
     for v in vecs:
         assert abs(float(torch.tensor(v).norm()) - 1.0) < 1e-4
+
+
+def test_json_mode_completion_is_json_prefix(served, native):
+    """response_format json_object: every sampled token keeps the output a JSON-object prefix."""
+    loop, _, _ = served
+    st, body = post(loop, "/v1/chat/completions", {"messages": [{"role": "user", "content": "json please"}],
+                                                    "max_tokens": 24, "temperature": 0,
+                                                    "response_format": {"type": "json_object"}})
+    assert st == 200, body
+    text = json.loads(body)["choices"][0]["message"]["content"]
+    assert text.lstrip().startswith("{")
+    c = native.JsonConstraint()
+    assert c.advance(text.encode())
