@@ -8,6 +8,7 @@
 #include "../native/json_constrain.h"
 #include "../native/tokenizer.h"
 #include "../native/tool_calls.h"
+#include "../native/trace.h"
 
 namespace py = pybind11;
 using namespace hk;
@@ -105,6 +106,10 @@ void bind_serve(py::module_& m) {
       })
       .def_static("validate", &JsonConstraint::validate);
 
+  m.def("trace_available", &trace_available);
+  m.def("trace_push", &trace_push, py::arg("name"));
+  m.def("trace_pop", &trace_pop);
+
   m.def("render_tools_preamble", [](const std::string& tools_json) {
     return render_tools_preamble(Json::parse(tools_json));
   });
@@ -127,6 +132,7 @@ void bind_serve(py::module_& m) {
       .def("take_cancelled", &HttpServer::take_cancelled)
       .def("set_metric", &HttpServer::set_metric, py::arg("name"), py::arg("value"), py::arg("help") = "",
            py::arg("counter") = false)
+      .def("set_health", &HttpServer::set_health, py::arg("ok"), py::arg("reason") = "")
       .def("stats", [](const HttpServer& s) { return s.stats().dump(); })
       .def("render_chat", [](const HttpServer& s, const std::string& messages_json, const std::string& tmpl) {
         return s.render_chat(Json::parse(messages_json), tmpl.empty() ? s.resolve_template() : tmpl);

@@ -262,6 +262,15 @@ bool HttpServer::handle(int fd, const std::string& method, const std::string& pa
                         bool keep_alive) {
   if (path == "/healthz" || path == "/health") {
     if (method != "GET") return respond_error(fd, 405, "use GET", "method_not_allowed", keep_alive);
+    if (!healthy_) {
+      Json h = Json::object();
+      h.set("status", Json::string("unhealthy"));
+      {
+        std::lock_guard<std::mutex> g(mu_);
+        h.set("reason", Json::string(health_reason_));
+      }
+      return respond(fd, 503, "application/json", h.dump(), keep_alive);
+    }
     return respond(fd, 200, "text/plain", "ok", keep_alive);
   }
   if (path == "/metrics") return respond(fd, 200, "text/plain; version=0.0.4", metrics_text(), keep_alive);
@@ -409,7 +418,24 @@ void HttpServer::forget(uint64_t id) {
   pending_.erase(id);
 }
 
+void HttpServer::set_health(bool ok, const std::string& reason) {
+  {
+    std::lock_guard<std::mutex> g(mu_);
+    health_reason_ = reason;
+  }
+  healthy_ = ok;
+}
+
 bool HttpServer::handle_generate(int fd, const Json& j, bool chat, bool keep_alive, const std::string& native) {
+  if (!healthy_) {
+    requests_rejected_++;
+    std::string why;
+    {
+      std::lock_guard<std::mutex> g(mu_);
+      why = health_reason_;
+    }
+    return respond_error(fd, 503, "engine unavailable: " + why, "unavailable", keep_alive);
+  }
   ServeRequest r;
   r.kind = chat ? "chat" : "completion";
   std::string prompt_text;

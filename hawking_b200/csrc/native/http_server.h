@@ -85,6 +85,8 @@ class HttpServer {
   void fail(uint64_t id, int status, const std::string& message);
   std::vector<uint64_t> take_cancelled();  // requests whose client left or hit a stop string
   void set_metric(const std::string& name, double value, const std::string& help, bool counter);
+  // Unhealthy: /healthz answers 503 with the reason and new generation requests are refused.
+  void set_health(bool ok, const std::string& reason);
   Json stats() const;
 
   // Chat template rendering (exposed for tests). messages: [{"role", "content"}].
@@ -120,6 +122,8 @@ class HttpServer {
   uint64_t next_id_ = 1;
   std::map<std::string, std::pair<double, std::pair<std::string, bool>>> metrics_;
 
+  std::atomic<bool> healthy_{true};
+  std::string health_reason_;  // guarded by mu_
   std::atomic<uint64_t> requests_admitted_{0}, requests_finished_{0}, requests_rejected_{0},
       tokens_generated_{0}, prompt_tokens_{0};
 };

@@ -13,6 +13,8 @@ lane), crates/hawking-serve/src/lib.rs:785-1115 (prefill phase, decode phase, st
 from __future__ import annotations
 
 import itertools
+import json
+import os
 import time
 from dataclasses import dataclass, field
 from typing import Dict, List, Optional
@@ -22,6 +24,7 @@ import torch
 
 from .._ext import native
 from ..models.config import ModelConfig
+from ..utils.trace import trace
 from .kv_cache import PagedKVCache
 from .sampling import RequestRng, SamplingParams
 
@@ -52,7 +55,7 @@ class EngineStats:
 
 class Engine:
     def __init__(self, cfg: ModelConfig, model, kv: PagedKVCache, max_batch: int = 8, max_prefill_tokens: int = 512,
-                 policy: int = 0, use_graphs: bool = True):
+                 policy: int = 0, use_graphs: bool = True, ledger: Optional[bool] = None):
         self.cfg, self.model, self.kv = cfg, model, kv
         self.max_batch = max_batch
         self.max_prefill_tokens = max_prefill_tokens
@@ -63,6 +66,9 @@ class Engine:
         self.stats = EngineStats()
         self._host_ids = torch.zeros(model.max_rows, dtype=torch.int32).pin_memory()
         self.tokenizer = None  # token bytes for JSON-mode requests (set by the server)
+        # per-step cost ledger (HK_LEDGER=1 or ledger=True): host phases of every step, in us
+        self.ledger_on = (os.environ.get("HK_LEDGER", "0") == "1") if ledger is None else ledger
+        self.ledger: List[dict] = []
 
     # ---- construction helpers ----
     @staticmethod
@@ -164,7 +170,18 @@ class Engine:
     # ---- one step ----
     def step(self) -> List[tuple]:
         """Run one scheduler step. Returns [(request_id, token, finish_reason)] for sampled rows."""
-        plan = self.sched.schedule()
+        with trace("engine.step"):
+            return self._step()
+
+    def ledger_json(self) -> str:
+        """The per-step ledger as JSON lines (host microseconds per phase; the sample phase holds
+        the device synchronisation, so it carries the forward's device time)."""
+        return "\n".join(json.dumps(e) for e in self.ledger)
+
+    def _step(self) -> List[tuple]:
+        t0 = time.perf_counter()
+        with trace("schedule"):
+            plan = self.sched.schedule()
         items = plan.items
         if not items:
             return []
@@ -218,27 +235,35 @@ class Engine:
         greedy = all(it.greedy for it, _ in sample_rows)
         mode = "greedy" if greedy else "none"
         sampled: List[int] = []
+        t_sched = time.perf_counter()
+        t_fwd = t_smp = 0.0
         for c0, c1 in bounds:
+            ta = time.perf_counter()
             self.stats.h2d_bytes += m.inp.upload(ids[c0:c1], pos[c0:c1], slots[c0:c1], rseq[c0:c1], rctx[c0:c1])
             rows_here = [(it, r - c0) for it, r in sample_rows if c0 <= r < c1]
-            if self.use_graphs and decode_only and c1 - c0 == n:
-                m.graph_forward(c1 - c0, mode)
-                self.stats.graph_steps += 1
-                picks = [(it, r) for it, r in rows_here]
-            else:
-                k = len(rows_here)
-                if k == 0:
-                    m.forward(c1 - c0, "none", n_logits=-1)
+            with trace("forward"):
+                if self.use_graphs and decode_only and c1 - c0 == n:
+                    m.graph_forward(c1 - c0, mode)
+                    self.stats.graph_steps += 1
+                    picks = [(it, r) for it, r in rows_here]
                 else:
-                    if k == c1 - c0:
-                        m.forward(c1 - c0, mode)
+                    k = len(rows_here)
+                    if k == 0:
+                        m.forward(c1 - c0, "none", n_logits=-1)
                     else:
-                        m.logit_rows[:k].copy_(torch.tensor([r for _, r in rows_here], dtype=torch.int32),
-                                               non_blocking=True)
-                        m.forward(c1 - c0, mode, n_logits=k)
-                picks = [(it, j) for j, (it, _) in enumerate(rows_here)] if 0 < k < c1 - c0 else rows_here
+                        if k == c1 - c0:
+                            m.forward(c1 - c0, mode)
+                        else:
+                            m.logit_rows[:k].copy_(torch.tensor([r for _, r in rows_here], dtype=torch.int32),
+                                                   non_blocking=True)
+                            m.forward(c1 - c0, mode, n_logits=k)
+                    picks = [(it, j) for j, (it, _) in enumerate(rows_here)] if 0 < k < c1 - c0 else rows_here
+            tb = time.perf_counter()
+            t_fwd += tb - ta
             if rows_here:
-                sampled.extend(self._sample(picks, greedy))
+                with trace("sample"):
+                    sampled.extend(self._sample(picks, greedy))
+            t_smp += time.perf_counter() - tb
         if serial and sample_rows:  # back to the plan's item order (rows ran in wave order)
             by_id = {it.id: tok for (it, _), tok in zip(sample_rows, sampled)}
             sampled = [by_id[it.id] for it in items if it.id in by_id]
@@ -259,6 +284,12 @@ class Engine:
             out.append((e.id, e.token, e.finish))
         self.stats.steps += 1
         self.stats.tokens_generated += len(sampled)
+        if self.ledger_on:
+            t_end = time.perf_counter()
+            self.ledger.append({"step": self.stats.steps, "rows": n, "decode": decode_only,
+                                "sampled": len(sampled), "schedule_us": round((t_sched - t0) * 1e6, 1),
+                                "launch_us": round(t_fwd * 1e6, 1), "sample_sync_us": round(t_smp * 1e6, 1),
+                                "total_us": round((t_end - t0) * 1e6, 1)})
         if decode_only:
             self.stats.decode_rows += n
         else:

@@ -7,6 +7,12 @@ while prompts prefill in budgeted chunks), and pushing the sampled tokens back
 response. Client disconnects and stop strings come back through ``take_cancelled`` and abort the
 request in the engine. Embedding requests are answered between steps.
 
+Failure handling: an engine step that raises (including a tensor-parallel collective that timed
+out on a peer and reported it through its status word) fails every in-flight request with 503,
+aborts them in the engine, and marks the server unhealthy (``/healthz`` 503 with the reason, new
+generation requests refused). Latency metrics: TTFT (admission to first token) and inter-token
+latency quantiles over the most recent requests, exported as gauges on ``/metrics``.
+
 Parity: crates/hawking-serve/src/lib.rs:525-1121 (run: admission, Phase A prefill, Phase B decode,
 Phase C stream/release), crates/hawking-serve/src/http.rs:1410 (embeddings), :329-365 (metrics).
 """
@@ -14,7 +20,8 @@ from __future__ import annotations
 
 import threading
 import time
-from typing import Dict, List, Optional
+from collections import deque
+from typing import Deque, Dict, List, Optional
 
 from .._ext import native
 from ..engine.sampling import SamplingParams
@@ -47,6 +54,11 @@ class ServeLoop:
         self._to_engine: Dict[int, int] = {}
         self._stop = threading.Event()
         self.steps = 0
+        self.healthy = True
+        self._t_admit: Dict[int, float] = {}    # server request id -> admission time
+        self._t_last: Dict[int, float] = {}     # server request id -> last token time
+        self._ttft: Deque[float] = deque(maxlen=2048)
+        self._itl: Deque[float] = deque(maxlen=8192)
 
     @property
     def port(self) -> int:
@@ -80,6 +92,7 @@ class ServeLoop:
                 continue
             self._to_server[erid] = r.id
             self._to_engine[r.id] = erid
+            self._t_admit[r.id] = time.perf_counter()
 
     def _cancel(self) -> None:
         for sid in self.server.take_cancelled():
@@ -94,18 +107,38 @@ class ServeLoop:
         self._cancel()
         if not self.engine.has_work():
             return 0
-        events = self.engine.step()
+        try:
+            events = self.engine.step()
+            tp = getattr(getattr(self.engine, "model", None), "tp", None)
+            if tp is not None and self.steps % 16 == 0:
+                tp.check()  # a peer's collective timed out (device status word)
+        except Exception as e:  # noqa: BLE001 - the step failed: drain and report
+            self._engine_failed(e)
+            return 0
         self.steps += 1
         pushed = 0
+        now = time.perf_counter()
         for erid, tok, fin in events:
             sid = self._to_server.get(erid)
             if sid is None:
                 continue
             self.server.push(sid, [int(tok)] if tok >= 0 else [], int(fin))
             pushed += 1
+            last = self._t_last.get(sid)
+            if last is None:
+                t0 = self._t_admit.get(sid)
+                if t0 is not None:
+                    self._ttft.append((now - t0) * 1000.0)
+            else:
+                self._itl.append((now - last) * 1000.0)
+            self._t_last[sid] = now
             if fin:
                 self._to_server.pop(erid, None)
                 self._to_engine.pop(sid, None)
+                self._t_admit.pop(sid, None)
+                self._t_last.pop(sid, None)
+        if self.steps % 16 == 0:
+            self._latency_metrics()
         st = getattr(self.engine, "stats", None)
         if st is not None and self.steps % 16 == 0:
             self.server.set_metric("hawking_engine_steps_total", st.steps, "Engine steps", True)
@@ -114,6 +147,32 @@ class ServeLoop:
             self.server.set_metric("hawking_gpu_readback_bytes_total", st.d2h_bytes,
                                    "Cumulative device-to-host readback bytes", True)
         return pushed
+
+    def _engine_failed(self, err: Exception) -> None:
+        msg = f"engine step failed: {type(err).__name__}: {err}"
+        self.healthy = False
+        self.server.set_health(False, msg)
+        for sid, erid in list(self._to_engine.items()):
+            self.server.fail(sid, 503, msg)
+            try:
+                self.engine.abort(erid)
+            except Exception:  # noqa: BLE001 - best effort while draining
+                pass
+        self._to_engine.clear()
+        self._to_server.clear()
+        self._t_admit.clear()
+        self._t_last.clear()
+
+    def _latency_metrics(self) -> None:
+        import numpy as np
+        for name, xs, what in (("hawking_ttft_ms", self._ttft, "Time to first token"),
+                               ("hawking_itl_ms", self._itl, "Inter-token latency")):
+            if not xs:
+                continue
+            a = np.asarray(xs)
+            for q in (50, 95, 99):
+                self.server.set_metric(f"{name}_p{q}", float(np.percentile(a, q)),
+                                       f"{what} p{q} over the last {len(a)} samples, ms", False)
 
     def run(self, max_seconds: Optional[float] = None) -> None:
         t_end = None if max_seconds is None else time.time() + max_seconds

@@ -27,15 +27,18 @@ def _sources(*patterns):
 
 
 CXX_FLAGS = ["-O3", "-std=c++17", "-pthread", "-fvisibility=hidden", "-Wno-unused-function"]
+CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 
 ext_modules = [
     Extension(
         "hawking_b200._native",
         sources=_sources("native/*.cpp", "bindings/native_module.cpp", "bindings/formats_bindings.cpp",
                          "bindings/engine_bindings.cpp", "bindings/serve_bindings.cpp"),
-        include_dirs=[pybind11.get_include(), os.path.join(ROOT, CSRC)],
+        # the CUDA toolkit's header-only NVTX (trace ranges) when present; no CUDA library is linked
+        include_dirs=[pybind11.get_include(), os.path.join(ROOT, CSRC)] + (
+            [os.path.join(CUDA_HOME, "include")] if os.path.isdir(os.path.join(CUDA_HOME, "include", "nvtx3")) else []),
         extra_compile_args=CXX_FLAGS,
-        extra_link_args=["-pthread"],
+        extra_link_args=["-pthread", "-ldl"],
         language="c++",
     )
 ]

@@ -179,3 +179,46 @@ def test_hawking_native_routes(served):
     assert eng.params[-1].temperature == 0.0
     st, _ = call(loop, "POST", "/v1/hawking/generate", {"prompt": ""})
     assert st == 400
+
+
+class Failing(Scripted):
+    """Raises on its third step (a failed collective, say)."""
+
+    def __init__(self, tok, script):
+        super().__init__(tok, script)
+        self.n = 0
+
+    def step(self):
+        self.n += 1
+        if self.n == 3:
+            raise RuntimeError("tensor-parallel collective reported device error 3 (peer timeout)")
+        return super().step()
+
+
+def test_engine_failure_drains_and_reports_unhealthy(native):
+    tok = native.Tokenizer.from_spec(bpe_spec(native))
+    eng = Failing(tok, " hello world hello there hello")
+    loop = ServeLoop(eng, tok, port=0, model_id="m").start()
+    th = loop.run_in_thread()
+    try:
+        assert call(loop, "GET", "/healthz")[0] == 200
+        st, body = call(loop, "POST", "/v1/completions", {"prompt": "hi", "max_tokens": 50})
+        assert st == 503 and "peer timeout" in body
+        st, body = call(loop, "GET", "/healthz")
+        assert st == 503 and json.loads(body)["status"] == "unhealthy"
+        assert call(loop, "POST", "/v1/completions", {"prompt": "again", "max_tokens": 5})[0] == 503
+        assert not eng.reqs  # the in-flight request was aborted in the engine
+    finally:
+        loop.stop()
+        th.join(timeout=5)
+
+
+def test_latency_quantiles_on_metrics(served):
+    loop, _, _ = served
+    for _ in range(3):
+        assert call(loop, "POST", "/v1/completions", {"prompt": "hi", "max_tokens": 6})[0] == 200
+    loop._latency_metrics()
+    st, text = call(loop, "GET", "/metrics")
+    assert st == 200
+    for name in ("hawking_ttft_ms_p50", "hawking_ttft_ms_p99", "hawking_itl_ms_p95"):
+        assert name in text, text
