@@ -131,6 +131,11 @@ class Engine:
         return Engine(cfg, model, kv, max_batch=max_batch, max_prefill_tokens=8 * max_batch, policy=policy)
 
     @staticmethod
+    def from_config(cfg: ModelConfig, weights, config, device="cuda", tp=None) -> "Engine":
+        """Engine.build with a typed ``hawking_b200.config.EngineConfig``."""
+        return Engine.build(cfg, weights, device=device, tp=tp, **config.build_kwargs())
+
+    @staticmethod
     def from_gguf(path: str, device="cuda", max_batch: int = 8, max_ctx: Optional[int] = None, **kw):
         """Load a GGUF model (weights re-laid for the kernels) and build an engine around it."""
         from ..formats.gguf import GgufModel

@@ -82,3 +82,15 @@ def test_serve_deepseek_preset_completion():
     finally:
         loop.stop()
         th.join(timeout=10)
+
+
+def test_cli_generate_preset(capsys):
+    """``python -m hawking_b200 generate`` end to end on random-weight presets."""
+    import json as _json
+
+    from hawking_b200.__main__ import main
+    for preset in ("deepseek-v3", "qwen3-next"):
+        assert main(["generate", "--preset", preset, "--layers", "4", "--prompt", "hello", "--max-tokens", "4",
+                     "--max-ctx", "256", "--json"]) == 0
+        out = _json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+        assert 1 <= len(out["tokens"]) <= 4
