@@ -88,7 +88,7 @@ void bind_serve(py::module_& m) {
       .def_readonly("stop_ids", &ServeRequest::stop_ids);
 
   py::class_<JsonConstraint>(m, "JsonConstraint")
-      .def(py::init<>())
+      .def(py::init<bool>(), py::arg("lenient_whitespace") = false)
       .def("accepts", [](const JsonConstraint& c, const py::bytes& b) { return c.accepts(std::string(b)); })
       .def("advance", [](JsonConstraint& c, const py::bytes& b) { return c.advance(std::string(b)); })
       .def_property_readonly("done", &JsonConstraint::done)

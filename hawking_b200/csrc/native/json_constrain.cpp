@@ -26,6 +26,12 @@ bool JsonConstraint::end_number() {
 }
 
 bool JsonConstraint::step(uint8_t c) {
+  if (!lenient_ && mode_ != Mode::Str && mode_ != Mode::Num && ws(c)) {
+    if (mode_ == Mode::Start || ws_run_ >= 1) return false;  // progress: no leading / repeated whitespace
+    ++ws_run_;
+  } else if (mode_ != Mode::Num || !ws(c)) {
+    ws_run_ = 0;
+  }
   auto after_close = [&] { mode_ = stack_.empty() ? Mode::Done : Mode::After; };
   auto begin_value = [&](uint8_t ch) -> bool {
     switch (ch) {
@@ -180,7 +186,7 @@ void JsonConstraint::mask(const Tokenizer& tok, float* logits, int64_t n) const 
 }
 
 bool JsonConstraint::validate(const std::string& text) {
-  JsonConstraint c;
+  JsonConstraint c(true);
   for (unsigned char ch : text)
     if (!c.step(ch)) return false;
   return c.done();

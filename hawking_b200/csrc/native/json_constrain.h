@@ -5,7 +5,10 @@
 // The state is the container stack plus the position inside the current token class (string with
 // escape / \u digits, number sub-states, literal remainder). A candidate token is accepted when
 // every byte of its text is a valid continuation; end-of-generation tokens are accepted only once
-// the top-level object is complete. Whitespace is allowed wherever JSON allows it.
+// the top-level object is complete. For generation (the default) the output must start with '{'
+// and whitespace comes at most one byte at a time outside strings, so every accepted token makes
+// progress (an unconstrained model could otherwise emit whitespace forever); `lenient_whitespace`
+// accepts any whitespace JSON allows (validation of complete texts).
 //
 // Parity: crates/hawking-core/src/json_constrain.rs (JsonConstraint::{advance, mask_logits,
 // is_done, validate}, JsonVocabIndex).
@@ -20,7 +23,7 @@ class Tokenizer;
 
 class JsonConstraint {
  public:
-  JsonConstraint() = default;
+  explicit JsonConstraint(bool lenient_whitespace = false) : lenient_(lenient_whitespace) {}
   // Whether `bytes` (a token's text) can follow the current state.
   bool accepts(const std::string& bytes) const;
   // Consume `bytes` (must be accepted); returns false (state unchanged) when it is not.
@@ -44,6 +47,8 @@ class JsonConstraint {
   uint8_t esc_ = 0;           // 0 none, 1 after '\', 2..5 hex digits of \uXXXX left + 1
   uint8_t num_ = 0;           // number sub-state (see json_constrain.cpp)
   std::string lit_;           // remaining bytes of true / false / null
+  bool lenient_ = false;
+  uint8_t ws_run_ = 0;        // consecutive whitespace bytes outside strings
 };
 
 }  // namespace hk

@@ -126,3 +126,20 @@ def test_tiny_mixtral_logits_match_cpu_oracle(tiny_moe_gguf, native):
     assert err < 3e-2 * np.abs(ref).max(), err
     out = eng.generate([prompt], SamplingParams(max_tokens=6))[0]
     assert len(out) == 6
+
+
+def test_decode_bitwise_deterministic(tiny_gguf):
+    """Two runs of the same teacher-forced forward and greedy generation agree bitwise (the GEMV
+    decode path has no atomics; split-KV merges in a fixed order)."""
+    m = GgufModel(tiny_gguf)
+    cfg = config_from_gguf(m).with_(max_ctx=256)
+    w = load_llama_weights(m, cfg, "cuda")
+    outs = []
+    for _ in range(2):
+        eng = Engine.build(cfg, w, device="cuda", max_batch=2, max_ctx=256, block_size=16, num_blocks=64, max_rows=8)
+        logits = eng.model.forward_tokens(list(range(40, 47)), seq_id=5)
+        toks = eng.generate([list(range(60, 70))], SamplingParams(max_tokens=8))[0]
+        assert bool(torch.isfinite(logits).all())
+        outs.append((logits.cpu(), toks))
+    assert torch.equal(outs[0][0], outs[1][0])
+    assert outs[0][1] == outs[1][1]

@@ -20,7 +20,7 @@ from test_tokenizer import bpe_spec
                                   '{"u": "\\u00e9\\n", "n": 0.25}'])
 def test_json_constraint_accepts_complete_objects(native, text):
     assert native.JsonConstraint.validate(text)
-    c = native.JsonConstraint()
+    c = native.JsonConstraint(lenient_whitespace=True)
     for ch in text.encode():  # byte by byte, every prefix is acceptable
         assert c.advance(bytes([ch])), (text, ch)
     assert c.done
@@ -30,6 +30,15 @@ def test_json_constraint_accepts_complete_objects(native, text):
                                   '{"a": 1}}', '"s"', '{"a": 1.}'])
 def test_json_constraint_rejects(native, text):
     assert not native.JsonConstraint.validate(text)
+
+
+def test_json_constraint_generation_makes_progress(native):
+    c = native.JsonConstraint()
+    assert not c.accepts(b" ") and not c.accepts(b"\n")  # the object starts at once
+    assert c.advance(b'{"a": 1,')
+    assert c.accepts(b" ") and not c.accepts(b"  ")   # one whitespace byte at a time
+    assert c.advance(b" ") and not c.accepts(b"\n")
+    assert c.accepts(b'"k "')                          # inside strings anything printable goes
 
 
 def test_json_constraint_token_choice(native):
