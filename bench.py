@@ -194,7 +194,7 @@ def bench_qwen_next(args):
                    "complete_bpw": round(complete_bpw, 3),
                    "l2": "inputs larger than L2: %.1f GB of weights resident" % ((w.table.nbytes + w.embed.nbytes) / 1e9)},
         "clocks": clocks, "e2e": e2e, "ttft_ms": ttft, "ttft_prompt": args.e2e_ctx,
-        "ttft_note": "prompts prefill token by token (no chunked DeltaNet prefill yet)",
+        "ttft_note": "prompts prefill in 8-token runs per forward (the DeltaNet kernels walk a run token by token, state in registers); no chunked WY form",
         "gpu_launches": launches * K,
         "bs8": {"tok_s_aggregate": round(8 * 1000.0 / ms8, 1), "ms_per_step": round(ms8, 4), "clocks": clocks8},
         "weights_gb": round((w.table.nbytes + w.embed.nbytes) / 1e9, 2),

@@ -25,13 +25,16 @@ from typing import List, Optional
 def _cmd_generate(a) -> int:
     from ._ext import native
     from .engine.sampling import SamplingParams
+    from .config import runtime_profile
+    extra = {k: v for k, v in runtime_profile(a.profile).engine.items() if k != "max_batch"}
     if a.gguf:
         from .engine.engine import Engine
-        eng = Engine.from_gguf(a.gguf, max_batch=1, max_ctx=a.max_ctx)
+        eng = Engine.from_gguf(a.gguf, max_batch=1, max_ctx=a.max_ctx, **extra)
         tok = native().Tokenizer.from_gguf(native().GgufFile.open(a.gguf))
     else:
         from .serve.__main__ import preset_engine
-        eng, tok = preset_engine(a.preset, a.layers, 1, a.max_ctx)
+        eng, tok = preset_engine(a.preset, a.layers, 1, a.max_ctx, **extra)
+    eng.apply_profile(a.profile)
     ids = tok.encode(a.prompt, True)
     p = SamplingParams(temperature=a.temperature, top_p=a.top_p, top_k=a.top_k, seed=a.seed, max_tokens=a.max_tokens,
                        stop_ids=list(tok.eog_ids()))
@@ -40,6 +43,8 @@ def _cmd_generate(a) -> int:
     out = eng.generate([ids], p)[0]
     dt = time.perf_counter() - t0
     text = tok.decode([t for t in out if not tok.is_eog(t)])
+    if a.stats:
+        print(json.dumps(eng.stats_json()), file=sys.stderr)
     if a.json:
         print(json.dumps({"text": text, "tokens": out, "prompt_tokens": len(ids), "seconds": round(dt, 4)}))
     else:
@@ -176,6 +181,8 @@ def main(argv: Optional[List[str]] = None) -> int:
     g.add_argument("--top-k", type=int, default=0)
     g.add_argument("--seed", type=int, default=42)
     g.add_argument("--json", action="store_true")
+    g.add_argument("--profile", default="default", help="runtime profile: default, fast, race, efficient, exact")
+    g.add_argument("--stats", action="store_true", help="print the engine's stats JSON to stderr")
     t = sub.add_parser("tokenize", help="text <-> token ids")
     t.add_argument("--gguf", required=True)
     t.add_argument("text")

@@ -2,14 +2,14 @@
 environment overrides the runtime reads (documented here with their defaults).
 
 Parity: crates/hawking-core/src/engine.rs:33-101 (EngineConfig), crates/hawking-serve/src/lib.rs:
-359-450 (ServeOptions), crates/hawking-core/src/lib.rs:198-226 (env helpers); the reference's
+359-450 (ServeOptions), :34-200 (RuntimeProfile -> LeverPlan, profile contracts), crates/hawking-core/src/lib.rs:198-226 (env helpers); the reference's
 284-flag sprawl (workspace/docs/reference/env_flags.md) is deliberately not reproduced.
 """
 from __future__ import annotations
 
 import os
-from dataclasses import asdict, dataclass
-from typing import Optional
+from dataclasses import asdict, dataclass, field
+from typing import Dict, Optional
 
 # name -> (default, meaning)
 ENV_FLAGS = {
@@ -20,6 +20,7 @@ ENV_FLAGS = {
     "HK_GEMM_SERIALIZE": ("unset", "debug: tensor-core GEMM issues each stage only after the previous one retired"),
     "HK_BOUNDS": ("0", "build time: compile index guards into the kernels (setup.py)"),
     "HK_SKIP_CUDA": ("0", "build time: build only the host (C++) module"),
+    "HK_STARTUP_TIMING": ("0", "Engine.from_gguf prints its load phases (open, config, weights, engine) as JSON"),
     "NCCL_NVLS_ENABLE": ("library default", "NCCL NVLink SHARP; the multi-GPU tests set 0"),
 }
 
@@ -45,3 +46,63 @@ class EngineConfig:
 
     def build_kwargs(self) -> dict:
         return asdict(self)
+
+
+@dataclass(frozen=True)
+class LeverPlan:
+    """What a runtime profile changes. ``engine`` overrides EngineConfig fields, ``model`` sets
+    attributes on the built model (only those it has), ``serve`` sets ServeLoop options."""
+    engine: Dict[str, object] = field(default_factory=dict)
+    model: Dict[str, object] = field(default_factory=dict)
+    serve: Dict[str, object] = field(default_factory=dict)
+    contract: str = ""
+
+
+# The levers this engine has: batch width and prefill budget (EngineConfig), the scheduler policy,
+# the row count from which dense Q4_K projections leave the W4A8 dp4a GEMV for the W4A16 tensor-core
+# GEMM (``tc_min_rows``; 1 = no int8 activation rounding at any batch), and the serving loop's
+# gather window (``gather_ms``: a step with free batch slots first waits this long for arrivals).
+RUNTIME_PROFILES: Dict[str, LeverPlan] = {
+    "default": LeverPlan(contract="profile=default: the configured engine, no profile-level trade."),
+    "fast": LeverPlan(engine={"max_prefill_tokens": 2048}, serve={"gather_ms": 0.0},
+                      contract="profile=fast: whole 2k prompts in one tensor-core forward; decode rows at "
+                               "batch <= 8 on the W4A8 GEMV (int8 activation blocks of 32)."),
+    "race": LeverPlan(engine={"max_prefill_tokens": 2048, "max_batch": 64, "policy": 1}, serve={"gather_ms": 0.0},
+                      contract="profile=race: fast + 64-wide decode batches, greedy-first scheduling; goal: "
+                               "aggregate tokens/s."),
+    "efficient": LeverPlan(engine={"max_prefill_tokens": 2048, "max_batch": 64}, serve={"gather_ms": 5.0},
+                           contract="profile=efficient: fast + a 5 ms gather window before a step with free "
+                                    "slots, so steps run wider (fewer weight passes per token: lower J/token) "
+                                    "at some inter-token latency."),
+    "exact": LeverPlan(model={"tc_min_rows": 1},
+                       contract="profile=exact: every dense Q4_K projection on the W4A16 tensor-core path "
+                                "(bf16 activations, fp32 accumulation): no int8 activation rounding; "
+                                "slower decode."),
+}
+
+
+def runtime_profile(name: str) -> LeverPlan:
+    """The lever plan of a named profile (default / fast / race / efficient / exact)."""
+    try:
+        return RUNTIME_PROFILES[name]
+    except KeyError:
+        raise ValueError(f"unknown runtime profile {name!r}; one of {sorted(RUNTIME_PROFILES)}") from None
+
+
+def apply_profile(config: EngineConfig, name: str) -> EngineConfig:
+    """``config`` with the profile's engine overrides applied (a new object)."""
+    plan = runtime_profile(name)
+    return EngineConfig(**{**asdict(config), **plan.engine})
+
+
+class MemoryBudgetError(MemoryError):
+    """A model or KV pool that does not fit the device is refused before anything is allocated."""
+
+
+def check_memory_budget(need_bytes: int, free_bytes: int, what: str, reserve_bytes: int = 1 << 30) -> None:
+    """Refuse ``what`` when ``need_bytes`` plus a working reserve exceeds ``free_bytes``.
+
+    Parity: crates/hawking-core/src/model/mod.rs:96-115 (memory budget refusal)."""
+    if need_bytes + reserve_bytes > free_bytes:
+        raise MemoryBudgetError(f"{what}: needs {need_bytes / 2**30:.2f} GiB + {reserve_bytes / 2**30:.2f} GiB "
+                                f"reserve, {free_bytes / 2**30:.2f} GiB free on the device")

@@ -78,8 +78,12 @@ __global__ void __launch_bounds__(128 * HPC) attn_prefill_kernel(AttnDecodeArgs 
   pdl_wait();
   const int tid = threadIdx.x, lane = tid & 31, warp = (tid >> 5) & 3, hl = tid >> 7;
   const int ntiles = (a.R + kPfBM - 1) / kPfBM;
-  const int tile = ntiles - 1 - (int)blockIdx.x;  // longest rows first
-  const int h = blockIdx.y * HPC + hl, g = (blockIdx.y * HPC) / (a.nh / a.nkv);
+  // blockIdx.x (the fastest-launched index) is the head group, so every head group's longest
+  // row tile is dispatched before any shorter tile (longest-first over the whole grid: the last
+  // wave holds only short causal tiles)
+  const int hg = (int)blockIdx.x;
+  const int tile = ntiles - 1 - (int)blockIdx.y;
+  const int h = hg * HPC + hl, g = (hg * HPC) / (a.nh / a.nkv);
   uint8_t* qs = qs_all + hl * kPfBM * HD * 2;  // this warp's head
   const int r0 = tile * kPfBM, nvalid = min(a.R - r0, kPfBM);
   if (tid < kPfBM) {
@@ -90,7 +94,7 @@ __global__ void __launch_bounds__(128 * HPC) attn_prefill_kernel(AttnDecodeArgs 
     const int hh = i / (kPfBM * CH), row = (i / CH) % kPfBM, c = i % CH;
     uint4 v = make_uint4(0u, 0u, 0u, 0u);
     if (row < nvalid) {
-      const float* src = a.q + ((int64_t)(r0 + row) * a.nh + blockIdx.y * HPC + hh) * HD + c * 8;
+      const float* src = a.q + ((int64_t)(r0 + row) * a.nh + hg * HPC + hh) * HD + c * 8;
       const float4 f0 = *reinterpret_cast<const float4*>(src), f1 = *reinterpret_cast<const float4*>(src + 4);
       v = make_uint4(pack_bf16(f0.x, f0.y), pack_bf16(f0.z, f0.w), pack_bf16(f1.x, f1.y), pack_bf16(f1.z, f1.w));
     }
@@ -315,7 +319,7 @@ void launch_prefill_hpc(const AttnDecodeArgs& a, cudaStream_t s, bool pdl) {
     HK_CUDA_CHECK(cudaFuncSetAttribute(attn_prefill_kernel<HD, HPC>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     configured = true;
   }
-  const dim3 grid((a.R + kPfBM - 1) / kPfBM, a.nh / HPC);
+  const dim3 grid(a.nh / HPC, (a.R + kPfBM - 1) / kPfBM);
   launch(attn_prefill_kernel<HD, HPC>, grid, dim3(128 * HPC), smem, s, pdl, a);
 }
 

@@ -15,6 +15,7 @@ from __future__ import annotations
 import itertools
 import json
 import os
+import sys
 import time
 from dataclasses import dataclass, field
 from typing import Dict, List, Optional
@@ -23,6 +24,7 @@ import numpy as np
 import torch
 
 from .._ext import native
+from ..config import check_memory_budget, env_flag
 from ..models.config import ModelConfig
 from ..utils.trace import trace
 from .kv_cache import PagedKVCache
@@ -51,6 +53,7 @@ class EngineStats:
     h2d_bytes: int = 0
     d2h_bytes: int = 0
     graph_steps: int = 0
+    step_s: float = 0.0   # wall time inside Engine.step()
 
 
 class Engine:
@@ -69,6 +72,8 @@ class Engine:
         # per-step cost ledger (HK_LEDGER=1 or ledger=True): host phases of every step, in us
         self.ledger_on = (os.environ.get("HK_LEDGER", "0") == "1") if ledger is None else ledger
         self.ledger: List[dict] = []
+        self.profile = "default"
+        self.startup: Dict[str, float] = {}  # load phases in ms (Engine.from_gguf)
 
     # ---- construction helpers ----
     @staticmethod
@@ -79,10 +84,13 @@ class Engine:
         from ..models.llama import LlamaModel
         max_ctx = max_ctx or cfg.max_ctx
         bpb = PagedKVCache.bytes_per_block(cfg.layers, cfg.n_kv_heads, cfg.head_dim, block_size)
+        free, _ = torch.cuda.mem_get_info(device)
         if num_blocks is None:
-            free, _ = torch.cuda.mem_get_info(device)
             num_blocks = int(free * kv_fraction // bpb)
             num_blocks = min(num_blocks, max_batch * (-(-max_ctx // block_size)) + 16)
+        # refuse a pool that cannot hold one full-context sequence, or that does not fit
+        check_memory_budget(max(num_blocks, -(-max_ctx // block_size)) * bpb, free,
+                            f"paged KV pool ({num_blocks} blocks of {block_size} tokens)", reserve_bytes=0)
         # one block-table row beyond max_batch: scratch sequences (embeddings) never starve
         kv = PagedKVCache(cfg.layers, cfg.n_kv_heads, cfg.head_dim, num_blocks, block_size, max_batch + 1,
                           -(-max_ctx // block_size), device)
@@ -141,12 +149,29 @@ class Engine:
         from ..formats.gguf import GgufModel
         from ..models.llama import load_llama_weights
         from ..models.torch_ref import config_from_gguf
+        timing = env_flag("HK_STARTUP_TIMING") == "1"
+        ph: Dict[str, float] = {}
+        t = time.perf_counter()
         m = GgufModel(path)
+        ph["open"] = (time.perf_counter() - t) * 1e3
+        t = time.perf_counter()
         cfg = config_from_gguf(m)
         if max_ctx:
             cfg = cfg.with_(max_ctx=max_ctx)
+        ph["config"] = (time.perf_counter() - t) * 1e3
+        free, _ = torch.cuda.mem_get_info(device)
+        check_memory_budget(sum(ti.nbytes for ti in m.tensors.values()), free, f"weights of {path}")
+        t = time.perf_counter()
         w = load_llama_weights(m, cfg, device)
-        return Engine.build(cfg, w, device=device, max_batch=max_batch, max_ctx=max_ctx, **kw)
+        torch.cuda.synchronize(device)
+        ph["weights"] = (time.perf_counter() - t) * 1e3
+        t = time.perf_counter()
+        eng = Engine.build(cfg, w, device=device, max_batch=max_batch, max_ctx=max_ctx, **kw)
+        ph["engine"] = (time.perf_counter() - t) * 1e3
+        eng.startup = {k: round(v, 2) for k, v in ph.items()}
+        if timing:
+            print(json.dumps({"startup_ms": eng.startup, "path": path}), file=sys.stderr, flush=True)
+        return eng
 
     # ---- requests ----
     def add_request(self, prompt: List[int], params: Optional[SamplingParams] = None) -> int:
@@ -175,8 +200,39 @@ class Engine:
     # ---- one step ----
     def step(self) -> List[tuple]:
         """Run one scheduler step. Returns [(request_id, token, finish_reason)] for sampled rows."""
+        t0 = time.perf_counter()
         with trace("engine.step"):
-            return self._step()
+            out = self._step()
+        self.stats.step_s += time.perf_counter() - t0
+        return out
+
+    def apply_profile(self, name: str):
+        """Set a runtime profile's model levers on this engine and drop captured graphs (the
+        profile's engine overrides are build-time: ``config.apply_profile`` then
+        ``Engine.from_config``). Returns the profile's LeverPlan."""
+        from ..config import runtime_profile
+        plan = runtime_profile(name)
+        for k, v in plan.model.items():
+            if hasattr(self.model, k):
+                setattr(self.model, k, v)
+        if hasattr(self.model, "release_graphs"):
+            self.model.release_graphs()
+        self.profile = name
+        return plan
+
+    def stats_json(self) -> dict:
+        """Counters since construction: steps, rows, tokens, host<->device bytes, graph replays,
+        decode tokens/s over the engine's step wall time, and the active profile.
+
+        Parity: crates/hawking-core/src/engine.rs:321-349 (GenStats::stats_json)."""
+        st = self.stats
+        out = {k: getattr(st, k) for k in st.__dataclass_fields__}
+        out["decode_tok_s"] = round(st.decode_rows / st.step_s, 2) if st.step_s > 0 else None
+        out["profile"] = self.profile
+        out["active_requests"] = len(self.requests)
+        if self.startup:
+            out["startup_ms"] = dict(self.startup)
+        return out
 
     def ledger_json(self) -> str:
         """The per-step ledger as JSON lines (host microseconds per phase; the sample phase holds

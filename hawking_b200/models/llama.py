@@ -226,6 +226,9 @@ class LlamaModel:
         self.part_lse = torch.zeros(cap * nh, device=self.dev)
         self.attn_counters = torch.zeros(R * nkv, dtype=torch.int32, device=self.dev)
         self.max_logit_rows = min(R, 256)  # rows whose logits one forward can return
+        # dense Q4_K forwards of at least this many rows run on the W4A16 tensor-core GEMM, smaller
+        # ones on the W4A8 dp4a GEMV (the runtime profile "exact" sets 1)
+        self.tc_min_rows = GEMV_COLS + 1
         self.logits = torch.zeros(self.max_logit_rows, weights.lm_head.N, device=self.dev)
         # set by the caller when the forward's rows hold long runs of one sequence (prefill chunks):
         # attention then runs on the tensor-core prefill kernel instead of the split-KV decode kernel
@@ -283,7 +286,7 @@ class LlamaModel:
 
     def use_tensor_cores(self, rows: int) -> bool:
         l0 = self.w.layers[0]
-        return rows > GEMV_COLS and all(w.fmt == GgmlType.Q4_K for w in l0.wqkv + [l0.wo]) and \
+        return rows >= self.tc_min_rows and all(w.fmt == GgmlType.Q4_K for w in l0.wqkv + [l0.wo]) and \
             l0.moe is None and l0.w_gu is not None and l0.w_gu.fmt == GgmlType.Q4_K and \
             l0.w_down.fmt == GgmlType.Q4_K
 
@@ -337,7 +340,8 @@ class LlamaModel:
             if advance:
                 ops.advance(inp.ids, self.next_ids, inp.positions, inp.row_ctx, rows)
             return
-        if tc and w.lm_head.fmt == GgmlType.Q4_K and nl > GEMV_COLS:  # (a few sampled rows: the GEMV)
+        # a few sampled rows take the GEMV, unless the tensor-core path was asked for at every size
+        if tc and w.lm_head.fmt == GgmlType.Q4_K and (nl > GEMV_COLS or self.tc_min_rows <= 1):
             ops.rmsnorm(x, w.out_norm, cfg.eps, yb=self.xb[:rows])
             src = self.xb[:rows]
             if n_logits:
