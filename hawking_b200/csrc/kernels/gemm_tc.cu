@@ -319,9 +319,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 // Q4_K super-block, two 128-byte swizzle atoms of A and of X); 64-wide stages with twice the
 // depth measured slower (the per-stage hand-offs dominate).
 //   warp 0 raw Q4_K TMA producer, warp 1 activation TMA producer, warp 2 TMEM owner + UMMA issuer,
-//   warps 4-11 dequantisers, warps 12-15 epilogue (TMEM lane quarter = warp % 4).
-constexpr int kPThreads = 512;
-constexpr int kPEpi0 = 12;
+//   warps 4-19 dequantisers (one 16-byte quant chunk per thread per stage), warps 20-23 epilogue
+//   (TMEM lane quarter = warp % 4).
+constexpr int kPThreads = 768;
+constexpr int kPDequantWarps = 16;  // four per SM sub-partition: the smem-load latency of one hides behind the others
+constexpr int kPEpi0 = kDequantWarp0 + kPDequantWarps;
 
 template <int BN>
 struct PLayout {
@@ -361,8 +363,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
   constexpr uint32_t tmem_cols = 2 * BN;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < PDR; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], kDequantWarps); }
-    for (int i = 0; i < PDA; ++i) { mbar_init(&a_full[i], kDequantWarps + 1); mbar_init(&a_empty[i], 1); }
+    for (int i = 0; i < PDR; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], kPDequantWarps); }
+    for (int i = 0; i < PDA; ++i) { mbar_init(&a_full[i], kPDequantWarps + 1); mbar_init(&a_empty[i], 1); }
     for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 4); }
     fence_barrier_init();
   }
@@ -442,11 +444,13 @@ __global__ void __launch_bounds__(kPThreads, 1)
       }
       if (ok) umma_commit(&acc_full[ab]);
     }
-  } else if (warp >= kDequantWarp0 && warp < kDequantWarp0 + kDequantWarps) {
-    // ---- dequantisers: thread (row r, chunk c) expands the 32 quant bytes of chunk c of the
-    // stage's half super-block (low nibbles: sub-block 4h + 2c, high: 4h + 2c + 1)
+  } else if (warp >= kDequantWarp0 && warp < kPEpi0) {
+    // ---- dequantisers: thread (row r, group c, half hf) expands quant bytes [32 c + 16 hf, +16)
+    // of the stage's half super-block: elements 16 hf.. of sub-block 4h + 2c (low nibbles) and of
+    // 4h + 2c + 1 (high nibbles). A warp covers 8 whole rows (512 contiguous bytes: no bank
+    // conflicts on the loads; the SW128 stores spread over all banks).
     const int tt = (warp - kDequantWarp0) * 32 + lane;
-    const int r = tt >> 1, c = tt & 1;
+    const int r = tt >> 2, c = (tt >> 1) & 1, hf = tt & 1;
     int it = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
@@ -455,8 +459,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
         ok = __shfl_sync(0xffffffffu, mbar_wait(&raw_full[rs], (it / PDR) & 1, a.status), 0);
         if (!ok) break;
         const uint4 hdr = *reinterpret_cast<const uint4*>(smem + L::off_hdr + rs * RAW_HDR + r * 16);
-        const uint4 q0 = *reinterpret_cast<const uint4*>(smem + L::off_qs + rs * RAW_QS + r * 64 + c * 32);
-        const uint4 q1 = *reinterpret_cast<const uint4*>(smem + L::off_qs + rs * RAW_QS + r * 64 + c * 32 + 16);
+        const uint4 q0 = *reinterpret_cast<const uint4*>(smem + L::off_qs + rs * RAW_QS + r * 64 + c * 32 + hf * 16);
         __syncwarp();
         if (lane == 0) mbar_arrive(&raw_empty[rs]);  // raw values are in registers now
         const int j0 = 4 * (s & 1) + 2 * c;
@@ -470,11 +473,12 @@ __global__ void __launch_bounds__(kPThreads, 1)
         ok = __shfl_sync(0xffffffffu, mbar_wait(&a_empty[as], ((it / PDA) & 1) ^ 1, a.status), 0);
         if (!ok) break;
         uint8_t* atom = smem + L::off_a + as * A_STAGE + c * A_ATOM;
-        const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+        const uint32_t w[4] = {q0.x, q0.y, q0.z, q0.w};
 #pragma unroll
-        for (int ch = 0; ch < 4; ++ch) {  // 16-byte chunk = 8 elements = 2 words
-          const uint2 lo0 = dq4(w[2 * ch], 0, s2A, o2A), lo1 = dq4(w[2 * ch + 1], 0, s2A, o2A);
-          const uint2 hi0 = dq4(w[2 * ch], 1, s2B, o2B), hi1 = dq4(w[2 * ch + 1], 1, s2B, o2B);
+        for (int k = 0; k < 2; ++k) {  // 16-byte chunk = 8 elements = 2 words
+          const int ch = 2 * hf + k;
+          const uint2 lo0 = dq4(w[2 * k], 0, s2A, o2A), lo1 = dq4(w[2 * k + 1], 0, s2A, o2A);
+          const uint2 hi0 = dq4(w[2 * k], 1, s2B, o2B), hi1 = dq4(w[2 * k + 1], 1, s2B, o2B);
           *reinterpret_cast<uint4*>(atom + sw128_offset(r, ch)) = make_uint4(lo0.x, lo0.y, lo1.x, lo1.y);
           *reinterpret_cast<uint4*>(atom + sw128_offset(r, ch + 4)) = make_uint4(hi0.x, hi0.y, hi1.x, hi1.y);
         }
@@ -552,6 +556,273 @@ __global__ void __launch_bounds__(kPThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, tmem_cols);
     tmem_relinquish();
+  }
+}
+
+// ---- CTA-pair persistent variant (cta_group::2) ------------------------------------------------
+// A 2-CTA cluster owns a 256-weight-row x 256-token tile: each CTA dequantises its own 128 weight
+// rows (A) and loads its own 128 tokens of the activation tile (B); rank 0 issues one
+// M = 256, N = 256 pair MMA per K = 16 slice that reads both CTAs' shared memory, and each CTA's
+// TMEM receives its 128 rows of the result. Per CTA this halves the activation bytes per FLOP
+// (the operand the one-CTA kernel waits on: a 64 KB activation stage per 1.1k-cycle MMA stage),
+// which leaves room for three operand stages. The peer's readiness reaches rank 0 through
+// cluster-scope mbarrier arrivals (its dequantisers directly; its activation copies through a
+// relay thread that waits for them locally); rank 0's commits arrive on both CTAs' barriers.
+// No TMA multicast: every load goes from global memory into the loading CTA's own shared memory.
+constexpr int kQDA = 3;  // operand stages
+constexpr uint32_t Q_X_ATOM = 128 * 128;  // 128 tokens x 64 bf16
+constexpr uint32_t Q_X_STAGE = 2 * Q_X_ATOM;
+struct QLayout {
+  static constexpr int DR = 2;
+  static constexpr uint32_t off_a = 0;
+  static constexpr uint32_t off_x = off_a + kQDA * A_STAGE;
+  static constexpr uint32_t off_hdr = off_x + kQDA * Q_X_STAGE;
+  static constexpr uint32_t off_qs = off_hdr + DR * RAW_HDR;
+  static constexpr uint32_t off_park = off_qs + DR * RAW_QS;
+  static constexpr uint32_t off_bar = off_park + 2 * 64 * 8 * 4;
+  static constexpr uint32_t n_bars = 2 * DR + 2 * kQDA + 4;
+  static constexpr uint32_t total = off_bar + n_bars * 8 + 16 + 1024;
+  static_assert(total <= 232448, "tc_gemm pair: shared memory over the 227 KB per-CTA limit");
+};
+
+template <bool SW>
+__global__ void __launch_bounds__(kPThreads, 1)
+    tc_gemm_q4k_pair(const __grid_constant__ CUtensorMap tm_hdr, const __grid_constant__ CUtensorMap tm_qs,
+                     const __grid_constant__ CUtensorMap tm_x, TcArgs a) {
+  using L = QLayout;
+  constexpr int PDR = L::DR, PDA = kQDA, BNP = 256;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::off_bar);
+  uint64_t* raw_full = bars;
+  uint64_t* raw_empty = bars + PDR;
+  uint64_t* a_full = bars + 2 * PDR;          // rank 0: the pair's stage is ready; rank 1: own copies landed
+  uint64_t* a_empty = bars + 2 * PDR + PDA;   // both: rank 0's MMAs on the stage completed
+  uint64_t* acc_full = bars + 2 * PDR + 2 * PDA;
+  uint64_t* acc_empty = acc_full + 2;         // rank 0: both CTAs drained the accumulator
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::n_bars);
+  float* park = reinterpret_cast<float*>(smem + L::off_park);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool lead = rank == 0;
+  constexpr int RB = SW ? BM / 2 : BM;
+  const int m_tiles = (a.M + BNP - 1) / BNP;
+  const int n_tiles = SW ? a.F / (2 * RB) : a.N / (2 * BM);
+  const int tiles = m_tiles * n_tiles;
+  const int nst = a.K / BK;
+  const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
+  constexpr uint32_t tmem_cols = 2 * BNP;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < PDR; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], kPDequantWarps); }
+    for (int i = 0; i < PDA; ++i) {
+      mbar_init(&a_full[i], lead ? 2 * kPDequantWarps + 2 : 1);
+      mbar_init(&a_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 8); }
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) { prefetch_tmap(&tm_hdr); prefetch_tmap(&tm_qs); prefetch_tmap(&tm_x); }
+  if (warp == 2) tmem_alloc_pair(tmem_slot, tmem_cols);
+  tc_fence_before();
+  cluster_sync_all();  // barriers of both CTAs initialised, TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (warp != 0) pdl_wait();
+
+  if (warp == 0 && lane == 0) {
+    // ---- raw Q4_K producer (this CTA's 128 weight rows) ----
+    int it = 0;
+    bool ok = true;
+    for (int t = pair; t < tiles && ok; t += pairs) {
+      const int n0 = (t / m_tiles) * 2 * RB + (int)rank * RB;
+      for (int s = 0; s < nst; ++s, ++it) {
+        const int slot = it % PDR;
+        if (!(ok = mbar_wait(&raw_empty[slot], ((it / PDR) & 1) ^ 1, a.status))) break;
+        const int sb = s >> 1, h = s & 1;
+        mbar_arrive_expect_tx(&raw_full[slot], RAW_HDR + RAW_QS);
+        uint8_t* hd = smem + L::off_hdr + slot * RAW_HDR;
+        uint8_t* qd = smem + L::off_qs + slot * RAW_QS;
+        if constexpr (SW) {
+          tma_load_2d(hd, &tm_hdr, sb * 16, n0, &raw_full[slot]);
+          tma_load_2d(hd + RAW_HDR / 2, &tm_hdr, sb * 16, a.F + n0, &raw_full[slot]);
+          tma_load_2d(qd, &tm_qs, (2 * sb + h) * 64, n0, &raw_full[slot]);
+          tma_load_2d(qd + RAW_QS / 2, &tm_qs, (2 * sb + h) * 64, a.F + n0, &raw_full[slot]);
+        } else {
+          tma_load_2d(hd, &tm_hdr, sb * 16, n0, &raw_full[slot]);
+          tma_load_2d(qd, &tm_qs, (2 * sb + h) * 64, n0, &raw_full[slot]);
+        }
+      }
+    }
+    for (int i = max(0, it - PDR); i < it; ++i) mbar_wait(&raw_full[i % PDR], (i / PDR) & 1, nullptr, 1u << 22);
+  } else if (warp == 1 && lane == 0) {
+    // ---- activation producer (this CTA's 128 tokens of the tile) ----
+    int it = 0;
+    bool ok = true;
+    for (int t = pair; t < tiles && ok; t += pairs) {
+      const int m0 = (t % m_tiles) * BNP + (int)rank * 128;
+      for (int s = 0; s < nst; ++s, ++it) {
+        const int slot = it % PDA;
+        if (!(ok = mbar_wait(&a_empty[slot], ((it / PDA) & 1) ^ 1, a.status))) break;
+        mbar_arrive_expect_tx(&a_full[slot], Q_X_STAGE);
+        uint8_t* xs = smem + L::off_x + slot * Q_X_STAGE;
+        tma_load_2d(xs, &tm_x, s * BK, m0, &a_full[slot]);
+        tma_load_2d(xs + Q_X_ATOM, &tm_x, s * BK + 64, m0, &a_full[slot]);
+      }
+    }
+    if (!ok) for (int k = 0; k < 2000; ++k) __nanosleep(100);
+  } else if (warp == 3 && lane == 0 && !lead) {
+    // ---- relay (rank 1): this CTA's activation stage landed -> count it on rank 0's barrier ----
+    int it = 0;
+    bool ok = true;
+    for (int t = pair; t < tiles && ok; t += pairs) {
+      for (int s = 0; s < nst; ++s, ++it) {
+        const int slot = it % PDA;
+        if (!(ok = mbar_wait(&a_full[slot], (it / PDA) & 1, a.status))) break;
+        mbar_arrive_cluster(&a_full[slot], 0);
+      }
+    }
+  } else if (warp == 2 && lane == 0 && lead) {
+    // ---- pair UMMA issuer ----
+    constexpr uint32_t idesc = idesc_bf16_f32(2 * BM, BNP);
+    int it = 0, j = 0;
+    bool ok = true;
+    for (int t = pair; t < tiles && ok; t += pairs, ++j) {
+      const int ab = j & 1;
+      if (!(ok = mbar_wait_cluster(&acc_empty[ab], ((j >> 1) & 1) ^ 1, a.status))) break;
+      tc_fence_after();
+      const uint32_t acc = tmem + (uint32_t)(ab * BNP);
+      for (int s = 0; s < nst; ++s, ++it) {
+        const int slot = it % PDA;
+        if (!(ok = mbar_wait_cluster(&a_full[slot], (it / PDA) & 1, a.status))) break;
+        tc_fence_after();
+        const uint32_t a_base = smem_u32(smem + L::off_a + slot * A_STAGE);
+        const uint32_t x_base = smem_u32(smem + L::off_x + slot * Q_X_STAGE);
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_f16_pair(acc, sdesc_k_sw128(a_base + c * A_ATOM + kk * 32), sdesc_k_sw128(x_base + c * Q_X_ATOM + kk * 32),
+                          idesc, (s | c | kk) != 0);
+        umma_commit_pair(&a_empty[slot], 0);
+        umma_commit_pair(&a_empty[slot], 1);
+      }
+      if (ok) {
+        umma_commit_pair(&acc_full[ab], 0);
+        umma_commit_pair(&acc_full[ab], 1);
+      }
+    }
+  } else if (warp >= kDequantWarp0 && warp < kPEpi0) {
+    // ---- dequantisers (this CTA's 128 rows; same mapping as the one-CTA persistent kernel) ----
+    const int tt = (warp - kDequantWarp0) * 32 + lane;
+    const int r = tt >> 2, c = (tt >> 1) & 1, hf = tt & 1;
+    int it = 0;
+    bool ok = true;
+    for (int t = pair; t < tiles && ok; t += pairs) {
+      for (int s = 0; s < nst; ++s, ++it) {
+        const int rs = it % PDR, as = it % PDA;
+        ok = __shfl_sync(0xffffffffu, mbar_wait(&raw_full[rs], (it / PDR) & 1, a.status), 0);
+        if (!ok) break;
+        const uint4 hdr = *reinterpret_cast<const uint4*>(smem + L::off_hdr + rs * RAW_HDR + r * 16);
+        const uint4 q0 = *reinterpret_cast<const uint4*>(smem + L::off_qs + rs * RAW_QS + r * 64 + c * 32 + hf * 16);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&raw_empty[rs]);
+        const int j0 = 4 * (s & 1) + 2 * c;
+        int sc0, mn0, sc1, mn1;
+        q4k_scale_min(j0, hdr.y, hdr.z, hdr.w, sc0, mn0);
+        q4k_scale_min(j0 + 1, hdr.y, hdr.z, hdr.w, sc1, mn1);
+        const float d = __half2float(__ushort_as_half((uint16_t)(hdr.x & 0xFFFF)));
+        const float dm = __half2float(__ushort_as_half((uint16_t)(hdr.x >> 16)));
+        const __nv_bfloat162 s2A = __float2bfloat162_rn(d * sc0), s2B = __float2bfloat162_rn(d * sc1);
+        const __nv_bfloat162 o2A = __float2bfloat162_rn(-dm * mn0), o2B = __float2bfloat162_rn(-dm * mn1);
+        ok = __shfl_sync(0xffffffffu, mbar_wait(&a_empty[as], ((it / PDA) & 1) ^ 1, a.status), 0);
+        if (!ok) break;
+        uint8_t* atom = smem + L::off_a + as * A_STAGE + c * A_ATOM;
+        const uint32_t w[4] = {q0.x, q0.y, q0.z, q0.w};
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          const int ch = 2 * hf + k;
+          const uint2 lo0 = dq4(w[2 * k], 0, s2A, o2A), lo1 = dq4(w[2 * k + 1], 0, s2A, o2A);
+          const uint2 hi0 = dq4(w[2 * k], 1, s2B, o2B), hi1 = dq4(w[2 * k + 1], 1, s2B, o2B);
+          *reinterpret_cast<uint4*>(atom + sw128_offset(r, ch)) = make_uint4(lo0.x, lo0.y, lo1.x, lo1.y);
+          *reinterpret_cast<uint4*>(atom + sw128_offset(r, ch + 4)) = make_uint4(hi0.x, hi0.y, hi1.x, hi1.y);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (lead) mbar_arrive(&a_full[as]);
+          else mbar_arrive_cluster(&a_full[as], 0);
+        }
+      }
+    }
+  } else if (warp >= kPEpi0) {
+    // ---- epilogue: this CTA's 128 weight rows x the tile's 256 tokens ----
+    const int q = warp & 3;
+    int j = 0;
+    for (int t = pair; t < tiles; t += pairs, ++j) {
+      const int ab = j & 1;
+      const bool ok = __shfl_sync(0xffffffffu, mbar_wait(&acc_full[ab], (j >> 1) & 1, a.status), 0);
+      if (!ok) break;
+      tc_fence_after();
+      const int n0 = (t / m_tiles) * 2 * RB + (int)rank * RB, m0 = (t % m_tiles) * BNP;
+      const uint32_t acc = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BNP);
+      if constexpr (SW) {
+        const int f = n0 + (q & 1) * 32 + lane;
+#pragma unroll 1
+        for (int cj = 0; cj < BNP / 8; ++cj) {
+          float v[8];
+          tmem_ld_x8(acc + cj * 8, v);
+          tmem_wait_ld();
+          float* slot = park + ((cj & 1) * 64 + (q & 1) * 32 + lane) * 8;
+          if (q >= 2) {
+            reinterpret_cast<float4*>(slot)[0] = make_float4(v[0], v[1], v[2], v[3]);
+            reinterpret_cast<float4*>(slot)[1] = make_float4(v[4], v[5], v[6], v[7]);
+          }
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          if (q < 2) {
+            const float4 u0 = reinterpret_cast<const float4*>(slot)[0], u1 = reinterpret_cast<const float4*>(slot)[1];
+            const float u[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const int m = m0 + cj * 8 + e;
+              if (m < a.M) a.h[(int64_t)m * a.h_stride + f] = __float2bfloat16(v[e] / (1.f + __expf(-v[e])) * u[e]);
+            }
+          }
+        }
+      } else {
+        const int n = n0 + q * 32 + lane;
+#pragma unroll 1
+        for (int cj = 0; cj < BNP / 8; ++cj) {
+          float v[8];
+          tmem_ld_x8(acc + cj * 8, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const int m = m0 + cj * 8 + e;
+            if (m < a.M && n < a.N) {
+              float* dst = a.y + (int64_t)m * a.y_stride + n;
+              if (a.atomic) atomicAdd(dst, v[e]);
+              else *dst = v[e];
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (lead) mbar_arrive(&acc_empty[ab]);
+        else mbar_arrive_cluster(&acc_empty[ab], 0);
+      }
+    }
+  }
+  tc_fence_before();
+  cluster_sync_all();  // no CTA leaves while its peer may still signal it or read the pair's TMEM
+  pdl_launch();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, tmem_cols);
+    tmem_relinquish_pair();
   }
 }
 
@@ -658,6 +929,62 @@ void launch_persistent(const TcGemmArgs& g, cudaStream_t s) {
          tm_qs, tm_x, a);
 }
 
+// True when the CTA-pair kernel covers the shape (whole 256-row weight pair tiles).
+bool pair_ok(const TcGemmArgs& g) {
+  const char* e = getenv("HK_GEMM_PAIR");
+  if (e && e[0] == '0') return false;
+  return g.bn == 256 && (g.h ? (g.N / 2) % 128 == 0 : g.N % 256 == 0);
+}
+
+template <bool SW>
+void launch_pair(const TcGemmArgs& g, cudaStream_t s) {
+  using L = QLayout;
+  const uint64_t rb = (uint64_t)g.w_row_bytes, hb = (uint64_t)g.w_hdr_row_bytes;
+  const uint32_t box_rows = SW ? BM / 2 : BM;
+  CUtensorMap tm_hdr = make_map_2d(CU_TENSOR_MAP_DATA_TYPE_UINT8, g.w_hdr, hb, g.N, hb, 16, box_rows,
+                                   CU_TENSOR_MAP_SWIZZLE_NONE);
+  CUtensorMap tm_qs = make_map_2d(CU_TENSOR_MAP_DATA_TYPE_UINT8, g.w, rb, g.N, rb, 64, box_rows, CU_TENSOR_MAP_SWIZZLE_NONE);
+  CUtensorMap tm_x = make_map_2d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, g.x, g.K, g.M, (uint64_t)g.x_stride * 2, 64, 128,
+                                 CU_TENSOR_MAP_SWIZZLE_128B);
+  TcArgs a{};
+  a.N = g.N;
+  a.K = g.K;
+  a.M = g.M;
+  a.stages_total = g.K / BK;
+  a.stages_per_split = a.stages_total;
+  a.y = g.y;
+  a.y_stride = g.y_stride;
+  a.atomic = g.atomic ? 1 : 0;
+  a.status = g.status;
+  a.h = g.h;
+  a.h_stride = g.h_stride;
+  a.F = g.N / 2;
+  static bool attr_set = false;
+  static int max_pairs = 0;
+  if (!attr_set) {
+    HK_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_q4k_pair<SW>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::total));
+    // pairs that can be resident at once (a pair needs two SMs of one TPC)
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2);
+    cfg.blockDim = dim3(kPThreads);
+    cfg.dynamicSmemBytes = L::total;
+    cudaLaunchAttribute at;
+    at.id = cudaLaunchAttributeClusterDimension;
+    at.val.clusterDim.x = 2;
+    at.val.clusterDim.y = 1;
+    at.val.clusterDim.z = 1;
+    cfg.attrs = &at;
+    cfg.numAttrs = 1;
+    HK_CUDA_CHECK(cudaOccupancyMaxActiveClusters(&max_pairs, tc_gemm_q4k_pair<SW>, &cfg));
+    if (max_pairs < 1) throw std::runtime_error("tc_gemm pair: no CTA pair fits on this device");
+    attr_set = true;
+  }
+  const int pair_tiles = ((g.M + 255) / 256) * (SW ? (g.N / 2) / 128 : g.N / 256);
+  const int pairs = std::max(1, std::min(pair_tiles, max_pairs));
+  launch_cluster(tc_gemm_q4k_pair<SW>, dim3(2 * pairs), dim3(kPThreads), L::total, s, g.pdl, 2, tm_hdr, tm_qs,
+                 tm_x, a);
+}
+
 }  // namespace
 
 int tc_gemm_splits(int N, int M, int K, int bn, int sms) {
@@ -676,6 +1003,11 @@ void tc_gemm_launch(const TcGemmArgs& g, cudaStream_t s) {
   if (g.persistent) {  // prefill-sized M: persistent CTAs, double-buffered TMEM accumulators
     if (g.bn != 256 && g.bn != 128) throw std::runtime_error("tc_gemm persistent: bn must be 128 or 256");
     if (g.h && g.N % 128) throw std::runtime_error("tc_gemm swiglu: F must be a multiple of 64");
+    if (pair_ok(g)) {  // CTA pairs: half the activation traffic per CTA, three operand stages
+      if (g.h) launch_pair<true>(g, s);
+      else launch_pair<false>(g, s);
+      return;
+    }
     if (g.h) {
       if (g.bn == 256) launch_persistent<256, true>(g, s);
       else launch_persistent<128, true>(g, s);

@@ -97,11 +97,16 @@ def test_tc_gemm_swiglu_epilogue(M, bn):
     _check(h.float(), ref)
 
 
-@pytest.mark.parametrize("M,N,swiglu", [(300, 512, False), (1000, 384, False), (520, 384, True), (257, 256, True)])
-def test_tc_gemm_persistent(M, N, swiglu):
+@pytest.mark.parametrize("pair", ["0", "1"])
+@pytest.mark.parametrize("M,N,swiglu", [(300, 512, False), (1000, 384, False), (520, 384, True), (257, 256, True),
+                                        (1000, 1024, False), (520, 512, True), (600, 8192, False)])
+def test_tc_gemm_persistent(M, N, swiglu, pair, monkeypatch):
     """Persistent tcgen05 GEMM (tiles looped per CTA, double-buffered TMEM accumulators), plain
-    store and fused SwiGLU epilogues, more tiles than CTAs and a ragged last token tile."""
+    store and fused SwiGLU epilogues, more tiles than CTAs and a ragged last token tile; with
+    pair=1 the CTA-pair (cta_group::2) kernel takes the shapes made of whole 256-row pair tiles
+    (N % 256, or F % 128 under SwiGLU), including more pair tiles than resident pairs."""
     from hawking_b200.ops import cat_rows
+    monkeypatch.setenv("HK_GEMM_PAIR", pair)
     K = 512
     g = torch.Generator(device=DEV).manual_seed(M + N)
     st = torch.zeros(1, dtype=torch.int32, device=DEV)
