@@ -17,7 +17,7 @@ ENV_FLAGS = {
     "HK_PREFETCH": ("0", "decode GEMVs prefetch the next projection's weights into L2 (measured slower; A/B only)"),
     "HK_TRACE": ("0", "NVTX ranges around engine phases (engine.step > schedule / forward / sample)"),
     "HK_LEDGER": ("0", "per-step host cost ledger kept on the engine (Engine.ledger_json())"),
-    "HK_GEMM_PAIR": ("1", "prefill GEMMs of whole 256-row weight pair tiles run on CTA pairs (cta_group::2); 0 = one-CTA kernel"),
+    "HK_GEMM_PAIR": ("0", "1: prefill GEMMs of whole 256-row weight pair tiles run on CTA pairs (cta_group::2)"),
     "HK_GEMM_SERIALIZE": ("unset", "debug: tensor-core GEMM issues each stage only after the previous one retired"),
     "HK_BOUNDS": ("0", "build time: compile index guards into the kernels (setup.py)"),
     "HK_SKIP_CUDA": ("0", "build time: build only the host (C++) module"),

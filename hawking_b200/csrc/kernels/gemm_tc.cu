@@ -932,7 +932,7 @@ void launch_persistent(const TcGemmArgs& g, cudaStream_t s) {
 // True when the CTA-pair kernel covers the shape (whole 256-row weight pair tiles).
 bool pair_ok(const TcGemmArgs& g) {
   const char* e = getenv("HK_GEMM_PAIR");
-  if (e && e[0] == '0') return false;
+  if (!e || e[0] != '1') return false;
   return g.bn == 256 && (g.h ? (g.N / 2) % 128 == 0 : g.N % 256 == 0);
 }
 
