@@ -319,10 +319,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 // Q4_K super-block, two 128-byte swizzle atoms of A and of X); 64-wide stages with twice the
 // depth measured slower (the per-stage hand-offs dominate).
 //   warp 0 raw Q4_K TMA producer, warp 1 activation TMA producer, warp 2 TMEM owner + UMMA issuer,
-//   warps 4-19 dequantisers (one 16-byte quant chunk per thread per stage), warps 20-23 epilogue
-//   (TMEM lane quarter = warp % 4).
-constexpr int kPThreads = 768;
-constexpr int kPDequantWarps = 16;  // four per SM sub-partition: the smem-load latency of one hides behind the others
+//   warps 4-11 dequantisers, warps 12-15 epilogue (TMEM lane quarter = warp % 4). (Sixteen
+//   dequantising warps with half the work each measured no faster.)
+constexpr int kPThreads = 512;
+constexpr int kPDequantWarps = kDequantWarps;
 constexpr int kPEpi0 = kDequantWarp0 + kPDequantWarps;
 
 template <int BN>
@@ -445,12 +445,10 @@ __global__ void __launch_bounds__(kPThreads, 1)
       if (ok) umma_commit(&acc_full[ab]);
     }
   } else if (warp >= kDequantWarp0 && warp < kPEpi0) {
-    // ---- dequantisers: thread (row r, group c, half hf) expands quant bytes [32 c + 16 hf, +16)
-    // of the stage's half super-block: elements 16 hf.. of sub-block 4h + 2c (low nibbles) and of
-    // 4h + 2c + 1 (high nibbles). A warp covers 8 whole rows (512 contiguous bytes: no bank
-    // conflicts on the loads; the SW128 stores spread over all banks).
+    // ---- dequantisers: thread (row r, chunk c) expands the 32 quant bytes of chunk c of the
+    // stage's half super-block (low nibbles: sub-block 4h + 2c, high: 4h + 2c + 1)
     const int tt = (warp - kDequantWarp0) * 32 + lane;
-    const int r = tt >> 2, c = (tt >> 1) & 1, hf = tt & 1;
+    const int r = tt >> 1, c = tt & 1;
     int it = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
@@ -459,7 +457,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
         ok = __shfl_sync(0xffffffffu, mbar_wait(&raw_full[rs], (it / PDR) & 1, a.status), 0);
         if (!ok) break;
         const uint4 hdr = *reinterpret_cast<const uint4*>(smem + L::off_hdr + rs * RAW_HDR + r * 16);
-        const uint4 q0 = *reinterpret_cast<const uint4*>(smem + L::off_qs + rs * RAW_QS + r * 64 + c * 32 + hf * 16);
+        const uint4 q0 = *reinterpret_cast<const uint4*>(smem + L::off_qs + rs * RAW_QS + r * 64 + c * 32);
+        const uint4 q1 = *reinterpret_cast<const uint4*>(smem + L::off_qs + rs * RAW_QS + r * 64 + c * 32 + 16);
         __syncwarp();
         if (lane == 0) mbar_arrive(&raw_empty[rs]);  // raw values are in registers now
         const int j0 = 4 * (s & 1) + 2 * c;
@@ -473,12 +472,11 @@ __global__ void __launch_bounds__(kPThreads, 1)
         ok = __shfl_sync(0xffffffffu, mbar_wait(&a_empty[as], ((it / PDA) & 1) ^ 1, a.status), 0);
         if (!ok) break;
         uint8_t* atom = smem + L::off_a + as * A_STAGE + c * A_ATOM;
-        const uint32_t w[4] = {q0.x, q0.y, q0.z, q0.w};
+        const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
-        for (int k = 0; k < 2; ++k) {  // 16-byte chunk = 8 elements = 2 words
-          const int ch = 2 * hf + k;
-          const uint2 lo0 = dq4(w[2 * k], 0, s2A, o2A), lo1 = dq4(w[2 * k + 1], 0, s2A, o2A);
-          const uint2 hi0 = dq4(w[2 * k], 1, s2B, o2B), hi1 = dq4(w[2 * k + 1], 1, s2B, o2B);
+        for (int ch = 0; ch < 4; ++ch) {  // 16-byte chunk = 8 elements = 2 words
+          const uint2 lo0 = dq4(w[2 * ch], 0, s2A, o2A), lo1 = dq4(w[2 * ch + 1], 0, s2A, o2A);
+          const uint2 hi0 = dq4(w[2 * ch], 1, s2B, o2B), hi1 = dq4(w[2 * ch + 1], 1, s2B, o2B);
           *reinterpret_cast<uint4*>(atom + sw128_offset(r, ch)) = make_uint4(lo0.x, lo0.y, lo1.x, lo1.y);
           *reinterpret_cast<uint4*>(atom + sw128_offset(r, ch + 4)) = make_uint4(hi0.x, hi0.y, hi1.x, hi1.y);
         }
@@ -716,7 +714,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
   } else if (warp >= kDequantWarp0 && warp < kPEpi0) {
     // ---- dequantisers (this CTA's 128 rows; same mapping as the one-CTA persistent kernel) ----
     const int tt = (warp - kDequantWarp0) * 32 + lane;
-    const int r = tt >> 2, c = (tt >> 1) & 1, hf = tt & 1;
+    const int r = tt >> 1, c = tt & 1;
     int it = 0;
     bool ok = true;
     for (int t = pair; t < tiles && ok; t += pairs) {
@@ -725,7 +723,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
         ok = __shfl_sync(0xffffffffu, mbar_wait(&raw_full[rs], (it / PDR) & 1, a.status), 0);
         if (!ok) break;
         const uint4 hdr = *reinterpret_cast<const uint4*>(smem + L::off_hdr + rs * RAW_HDR + r * 16);
-        const uint4 q0 = *reinterpret_cast<const uint4*>(smem + L::off_qs + rs * RAW_QS + r * 64 + c * 32 + hf * 16);
+        const uint4 q0 = *reinterpret_cast<const uint4*>(smem + L::off_qs + rs * RAW_QS + r * 64 + c * 32);
+        const uint4 q1 = *reinterpret_cast<const uint4*>(smem + L::off_qs + rs * RAW_QS + r * 64 + c * 32 + 16);
         __syncwarp();
         if (lane == 0) mbar_arrive(&raw_empty[rs]);
         const int j0 = 4 * (s & 1) + 2 * c;
@@ -739,12 +738,11 @@ __global__ void __launch_bounds__(kPThreads, 1)
         ok = __shfl_sync(0xffffffffu, mbar_wait(&a_empty[as], ((it / PDA) & 1) ^ 1, a.status), 0);
         if (!ok) break;
         uint8_t* atom = smem + L::off_a + as * A_STAGE + c * A_ATOM;
-        const uint32_t w[4] = {q0.x, q0.y, q0.z, q0.w};
+        const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
-        for (int k = 0; k < 2; ++k) {
-          const int ch = 2 * hf + k;
-          const uint2 lo0 = dq4(w[2 * k], 0, s2A, o2A), lo1 = dq4(w[2 * k + 1], 0, s2A, o2A);
-          const uint2 hi0 = dq4(w[2 * k], 1, s2B, o2B), hi1 = dq4(w[2 * k + 1], 1, s2B, o2B);
+        for (int ch = 0; ch < 4; ++ch) {  // 16-byte chunk = 8 elements = 2 words
+          const uint2 lo0 = dq4(w[2 * ch], 0, s2A, o2A), lo1 = dq4(w[2 * ch + 1], 0, s2A, o2A);
+          const uint2 hi0 = dq4(w[2 * ch], 1, s2B, o2B), hi1 = dq4(w[2 * ch + 1], 1, s2B, o2B);
           *reinterpret_cast<uint4*>(atom + sw128_offset(r, ch)) = make_uint4(lo0.x, lo0.y, lo1.x, lo1.y);
           *reinterpret_cast<uint4*>(atom + sw128_offset(r, ch + 4)) = make_uint4(hi0.x, hi0.y, hi1.x, hi1.y);
         }
