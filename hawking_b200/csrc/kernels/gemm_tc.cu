@@ -459,8 +459,6 @@ __global__ void __launch_bounds__(kPThreads, 1)
         const uint4 hdr = *reinterpret_cast<const uint4*>(smem + L::off_hdr + rs * RAW_HDR + r * 16);
         const uint4 q0 = *reinterpret_cast<const uint4*>(smem + L::off_qs + rs * RAW_QS + r * 64 + c * 32);
         const uint4 q1 = *reinterpret_cast<const uint4*>(smem + L::off_qs + rs * RAW_QS + r * 64 + c * 32 + 16);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&raw_empty[rs]);  // raw values are in registers now
         const int j0 = 4 * (s & 1) + 2 * c;
         int sc0, mn0, sc1, mn1;
         q4k_scale_min(j0, hdr.y, hdr.z, hdr.w, sc0, mn0);
@@ -482,7 +480,13 @@ __global__ void __launch_bounds__(kPThreads, 1)
         }
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&a_full[as]);
+        if (lane == 0) {
+          mbar_arrive(&a_full[as]);
+          // the raw slot is released only after its values were consumed: releasing it right
+          // after the shared-memory loads let the next TMA write overtake a load (rows of the
+          // tile came out wrong in about one run in four)
+          mbar_arrive(&raw_empty[rs]);
+        }
       }
     }
   } else if (warp >= kPEpi0) {
@@ -725,8 +729,6 @@ __global__ void __launch_bounds__(kPThreads, 1)
         const uint4 hdr = *reinterpret_cast<const uint4*>(smem + L::off_hdr + rs * RAW_HDR + r * 16);
         const uint4 q0 = *reinterpret_cast<const uint4*>(smem + L::off_qs + rs * RAW_QS + r * 64 + c * 32);
         const uint4 q1 = *reinterpret_cast<const uint4*>(smem + L::off_qs + rs * RAW_QS + r * 64 + c * 32 + 16);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&raw_empty[rs]);
         const int j0 = 4 * (s & 1) + 2 * c;
         int sc0, mn0, sc1, mn1;
         q4k_scale_min(j0, hdr.y, hdr.z, hdr.w, sc0, mn0);
@@ -751,6 +753,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
         if (lane == 0) {
           if (lead) mbar_arrive(&a_full[as]);
           else mbar_arrive_cluster(&a_full[as], 0);
+          mbar_arrive(&raw_empty[rs]);  // after the raw values were consumed
         }
       }
     }
