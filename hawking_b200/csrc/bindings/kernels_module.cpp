@@ -351,4 +351,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   hk::register_more_kernels(m);
   hk::register_tp_kernels(m);
   hk::register_model_kernels(m);
+  hk::register_mg_kernels(m);
 }

@@ -104,6 +104,50 @@ void tp_argmax_launch(const TpArgmaxArgs& a, cudaStream_t s, bool pdl);
 
 void gemv_launch(int fmt, int epi, const GemvArgs& a, int nb, cudaStream_t s, bool pdl);
 
+// ---- full-precision small-batch GEMV on the tensor cores (mma_gemv.cu) ----
+// W4A16: weights in fragment-ordered tiles of 16 rows x 256 columns (mg_pack_launch), bf16
+// activations, fp32 accumulation. See mma_gemv.cu for the design.
+enum MgInput : int { MG_X_NORM = 0, MG_X_BF16 = 1, MG_X_FRAG = 2 };
+enum MgEpilogue : int { MG_STORE = 0, MG_RESID = 1, MG_SWIGLU = 2, MG_PUSH = 3 };
+struct MgArgs {
+  const uint8_t* tiles;     // [G row groups][KT column tiles][tile bytes]
+  int G, KT;                // row groups (16 rows each), 256-column tiles per row group
+  int N, K;                 // logical rows (STORE / RESID / PUSH) and columns
+  int nb;                   // batch columns 1..8
+  // input (one of):
+  const float* x_f32;       // MG_X_NORM: fp32 rows [nb, x_f32_stride], RMSNorm with norm_w (optional)
+  int64_t x_f32_stride;
+  const float* norm_w;
+  float eps;
+  const __nv_bfloat16* xb;  // MG_X_BF16: bf16 rows [nb, xb_stride]
+  int64_t xb_stride;
+  const uint4* xfrag;       // MG_X_FRAG: bf16 in B-fragment order, column n at n * xfrag_cstride uint4s
+  int64_t xfrag_cstride;
+  // outputs
+  float* y;                 // STORE / RESID: fp32 [nb, y_stride]
+  int64_t y_stride;
+  const float* bias;        // optional [N]
+  int F;                    // SWIGLU: output rows (tiles hold gate rows 8g..8g+7 then the matching up rows)
+  __nv_bfloat16* hfrag;     // SWIGLU: h in B-fragment order (column stride hfrag_cstride uint4s), and/or
+  int64_t hfrag_cstride;
+  __nv_bfloat16* hb;        //   h as plain bf16 rows [nb, hb_stride]
+  int64_t hb_stride;
+  unsigned long long* argmax_slots;  // STORE: fused greedy keys (as GemvArgs)
+  int64_t argmax_offset;
+  unsigned long long* const* push_recv;  // PUSH: as GemvArgs
+  const int* push_epoch;
+  int push_n;
+  // scratch: partial fragments [gridDim.x * 8 warps][2][32] float4, zeroed counters [G]
+  float4* part;
+  int* counters;
+  int* status;
+};
+int mg_tile_bytes(int fmt);
+size_t mg_smem_bytes(int fmt, int xin, int nb, int K);
+// rowmap[G * 16]: source row of each tile row (-1: zero row)
+void mg_pack_launch(int fmt, const WPlanes& w, const int* rowmap, int G, int KT, uint8_t* out, cudaStream_t s);
+void mg_gemv_launch(int fmt, int xin, int epi, const MgArgs& a, int grid, cudaStream_t s, bool pdl);
+
 // ---- decode ops (decode_ops.cu, attention.cu) ----
 
 // RMSNorm (optional weight) of rows of x, then q8 activation blocks. `norm=false` quantises x

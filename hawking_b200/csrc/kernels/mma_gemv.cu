@@ -1,0 +1,460 @@
+// Full-precision small-batch dequant GEMV (K1, batch 1..8): y[b, n] = sum_k W[n, k] * x[b, k] with
+// W in GGUF Q4_K and x in bf16 (W4A16), fp32 accumulation. Default decode path for batches <= 8.
+//
+// Design (sm_100a, batch <= 8 is a bandwidth problem with a small matrix multiply inside it):
+//  * Weight layout. At load time every [N, K] Q4_K matrix is re-laid (losslessly) into tiles of
+//    16 rows x 256 columns: the 16 rows' 16-byte super-block headers, then the 2048 quant bytes
+//    in the register-fragment order of mma.sync m16n8k16 (lane t of a warp finds the 8 nibbles of
+//    its A fragment for one k-step in one 32-bit word, four k-steps per 16-byte load). Tiles are
+//    stored row-group major, so any contiguous range of tiles is one contiguous byte range.
+//  * Streaming. The tiles are split into gridDim.x * 8 contiguous, equal ranges, one per warp. Each
+//    warp owns a 4-deep ring of tile buffers in shared memory filled by cp.async.bulk (the TMA copy
+//    engine, completing on an mbarrier); lane 0 issues the first four copies before the
+//    programmatic-dependent-launch wait, so a kernel's weights stream in while the kernel before it
+//    finishes. No multicast (the kernel may run in multi-GPU processes).
+//  * Math. A nibble n becomes the bf16 value 1 + n/16 with one shift and one lop3 (the nibble lands
+//    in the top four mantissa bits of 1.0). acc1 = sum_k (1 + n_k/16) x_k comes from mma.sync with
+//    fp32 accumulation, acc2 = sum_k x_k from a second mma against an all-ones fragment, and the
+//    sub-block's contribution d*sc*sum(n x) - dmin*mn*sum(x) = S16 * acc1 - (S16 + dmin*mn) * acc2
+//    with S16 = 16 * d * sc is applied in fp32 per 32-element sub-block. The weight enters the
+//    tensor core as exact small integers, so the only rounding of operands is x to bf16.
+//    Why mma.sync and not tcgen05 here: at batch <= 8 the dequantised A operand would have to be
+//    written to shared memory for tcgen05 (2 bytes per weight, then read again by the tensor core),
+//    which at the HBM weight rate exceeds the SM's shared-memory bandwidth; mma.sync takes A from
+//    registers, where the dequantisation leaves it.
+//  * Split-K fix-up, deterministic. A row group (16 rows) split over several warps: each writes its
+//    partial fragment to scratch (two slots per warp: the first and last row group of its range),
+//    bumps the row group's counter, and the warp that completes the count sums the partials in
+//    warp order (fixed, independent of arrival order), runs the epilogue and clears the counter.
+//  * Activations. x is staged in shared memory in the B-fragment order (from fp32 rows with a fused
+//    RMSNorm, or from bf16 rows), or read in that order from global memory (the SwiGLU epilogue of
+//    the gate/up GEMV writes h that way for the down projection, whose K is too wide to stage).
+//  * Epilogues: STORE (y = v + bias, optional fused greedy keys), RESID (y += v), SWIGLU (gate and
+//    up rows of the fused [gate | up] matrix are interleaved 8 + 8 in each tile, so one lane holds a
+//    gate value and its up value: h = silu(g) * u in registers), PUSH (tensor parallel: flagged
+//    words into every rank's receive region, as the dp4a GEMV's push epilogue).
+//
+// Every mbarrier wait is bounded (HK_ERR_MBAR_TIMEOUT in the status word); a warp that gives up
+// waits (bounded) for its own copies still in flight before it exits.
+//
+// Parity: crates/hawking-core/shaders/quant.metal gemm_q4_k_m_fused* (f32 activations, the
+// reference's default; its W4A8 GEMV is held off as quality-blocked in
+// workspace/docs/reference/env_flags.md:38); Q4_K formula crates/hawking-core/src/quant.rs:34-160.
+#include "mma_gemv.cuh"
+#include "sm100.cuh"
+#include "tp.cuh"
+
+namespace hk {
+namespace mg {
+
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+constexpr int kStages = 4;
+constexpr int kScaleBytes = 16 * 8 * 8;  // per warp: [16 rows][8 sub-blocks] float2 (S16, M'')
+
+template <int FMT> struct Tile;
+template <> struct Tile<WF_Q4_K> {
+  static constexpr int BYTES = 2304;  // 16 headers x 16 B + 16 rows x 128 quant bytes
+};
+
+__device__ __forceinline__ uint32_t and_or(uint32_t a, uint32_t mask, uint32_t magic) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(mask), "r"(magic));  // (a & mask) | magic
+  return d;
+}
+
+__device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pick(const uint4& v, int i) {
+  return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
+}
+
+// Decode the 16 rows' Q4_K scales of one tile into per-warp shared memory: (S16, M'') for every
+// (row, sub-block). Lane t handles row t/2, sub-blocks 4*(t&1) .. +3.
+__device__ __forceinline__ void decode_scales_q4k(const uint8_t* tile, float2* scs, int lane) {
+  const int row = lane >> 1, half = lane & 1;
+  const uint4 h = *reinterpret_cast<const uint4*>(tile + row * 16);
+  const float d = __half2float(__ushort_as_half((uint16_t)(h.x & 0xFFFF)));
+  const float dmin = __half2float(__ushort_as_half((uint16_t)(h.x >> 16)));
+  // 6-bit scales / mins of the four sub-blocks as bytes (GGUF get_scale_min_k4, four at a time)
+  const uint32_t scb = half ? ((h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u)) : (h.y & 0x3F3F3F3Fu);
+  const uint32_t mnb = half ? (((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u)) : (h.z & 0x3F3F3F3Fu);
+  const float d16 = 16.f * d;
+  const float c_sc = -d16 * 8388608.f, c_mn = -dmin * 8388608.f;
+  float v[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    // byte i placed in the mantissa of 2^23: the float 2^23 + byte, exact; one fma removes 2^23
+    // and applies the scale with a single rounding
+    const float scf = __uint_as_float(__byte_perm(scb, 0x4B000000u, 0x7650 + i));
+    const float mnf = __uint_as_float(__byte_perm(mnb, 0x4B000000u, 0x7650 + i));
+    const float s16 = fmaf(d16, scf, c_sc);
+    const float mt = fmaf(dmin, mnf, c_mn);
+    v[2 * i] = s16;
+    v[2 * i + 1] = s16 + mt;
+  }
+  float4* dst = reinterpret_cast<float4*>(scs + row * 8 + half * 4);
+  dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+  dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
+
+// 32-bit word index of the pair x[n][k], x[n][k + 1] (k even) in the B-fragment order. Column n
+// starts at n * cstride uint4s.
+__device__ __forceinline__ int64_t frag_u32(int n, int k, int64_t cstride) {
+  const int ks = k >> 4, kk = k & 15, q = (kk & 7) >> 1, reg = kk >> 3;
+  return ((int64_t)n * cstride + (((ks >> 2) * 4 + q) * 2 + ((ks & 3) >> 1))) * 4 + (ks & 1) * 2 + reg;
+}
+
+struct XFrag {
+  const uint4* p;   // shared or global (generic address)
+  int64_t cstride;  // uint4s between columns
+};
+
+// One tile: 16 rows x 256 columns (super-block s) accumulated into sum[4] (the lane's C fragment:
+// rows r0, r0 + 8 x columns 2q, 2q + 1).
+template <int NB>
+__device__ __forceinline__ void consume_q4k(const uint8_t* tile, int s, const XFrag& x, float2* scs, int lane,
+                                            float (&sum)[4]) {
+  decode_scales_q4k(tile, scs, lane);
+  const int n = lane >> 2, q = lane & 3, r0 = lane >> 2;
+  const uint4* qp = reinterpret_cast<const uint4*>(tile + 256) + lane;
+  uint4 qv[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) qv[j] = qp[j * 32];
+  __syncwarp();  // scales visible to every lane
+  const bool has_col = n < NB;
+  const uint4* xp = x.p + (int64_t)n * x.cstride + ((int64_t)(4 * s) * 4 + q) * 2;
+  constexpr uint32_t ONES = 0x3F803F80u;
+  constexpr uint32_t M = 0x00780078u;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {  // k-step groups of 4 (two sub-blocks)
+    uint4 b01 = make_uint4(0, 0, 0, 0), b23 = make_uint4(0, 0, 0, 0);
+    if (has_col) {
+      b01 = xp[j * 8];
+      b23 = xp[j * 8 + 1];
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {  // sub-block 2j + h = k-steps 4j + 2h, 4j + 2h + 1
+      const uint4 b = h ? b23 : b01;
+      float c[4] = {0.f, 0.f, 0.f, 0.f}, e[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int kk = 0; kk < 2; ++kk) {
+        const uint32_t w = pick(qv[j], 2 * h + kk);
+        const uint32_t bx = kk ? b.z : b.x, by = kk ? b.w : b.y;
+        mma_bf16(c, and_or(w << 3, M, ONES), and_or(w >> 1, M, ONES), and_or(w >> 5, M, ONES),
+                 and_or(w >> 9, M, ONES), bx, by);
+        mma_bf16(e, ONES, ONES, ONES, ONES, bx, by);
+      }
+      const int sb = 2 * j + h;
+      const float2 s0 = scs[r0 * 8 + sb], s1 = scs[(r0 + 8) * 8 + sb];
+      sum[0] = fmaf(s0.x, c[0], fmaf(-s0.y, e[0], sum[0]));
+      sum[2] = fmaf(s1.x, c[2], fmaf(-s1.y, e[2], sum[2]));
+      if (NB > 1) {
+        sum[1] = fmaf(s0.x, c[1], fmaf(-s0.y, e[1], sum[1]));
+        sum[3] = fmaf(s1.x, c[3], fmaf(-s1.y, e[3], sum[3]));
+      }
+    }
+  }
+  __syncwarp();  // every lane is done with the tile and the scales before they are overwritten
+}
+
+// Store the bf16 value of x[n][k] into a B-fragment-order buffer.
+__device__ __forceinline__ void frag_store_bf16(__nv_bfloat16* base, int64_t cstride, int n, int k, float v) {
+  base[frag_u32(n, k & ~1, cstride) * 2 + (k & 1)] = __float2bfloat16_rn(v);
+}
+
+template <int EPI>
+__device__ __forceinline__ void epilogue(const MgArgs& a, int64_t g, const float (&v)[4], int lane) {
+  const int r0 = lane >> 2, q = lane & 3;
+  if constexpr (EPI == MG_SWIGLU) {
+    const int64_t o = g * 8 + r0;  // output row: gate in tile row r0, up in r0 + 8
+    if (o >= a.F) return;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int col = 2 * q + i;
+      if (col < a.nb) {
+        const float gt = v[i], up = v[2 + i];
+        const float hv = gt / (1.f + __expf(-gt)) * up;
+        if (a.hfrag) frag_store_bf16(a.hfrag, a.hfrag_cstride, col, (int)o, hv);
+        if (a.hb) a.hb[(int64_t)col * a.hb_stride + o] = __float2bfloat16_rn(hv);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t row = g * 16 + (i >> 1) * 8 + r0;
+      const int col = 2 * q + (i & 1);
+      if (row >= a.N || col >= a.nb) continue;
+      float val = v[i];
+      if (a.bias) val += a.bias[row];
+      if constexpr (EPI == MG_PUSH) {
+        const uint32_t flag = (uint32_t)*a.push_epoch;
+        for (int p = 0; p < a.push_n; ++p)
+          ll_store(a.push_recv[p] + (int64_t)col * a.N + row, __float_as_uint(val), flag);
+      } else {
+        float* yp = a.y + (int64_t)col * a.y_stride + row;
+        if constexpr (EPI == MG_RESID) *yp += val;
+        else *yp = val;
+        if (EPI == MG_STORE && a.argmax_slots)
+          atomicMax(a.argmax_slots + (int64_t)col * kArgmaxSlots + (row % kArgmaxSlots),
+                    argmax_key(val, (int)(row + a.argmax_offset)));
+      }
+    }
+  }
+}
+
+// Stage the activations of `nb` columns into shared memory in B-fragment order.
+template <int XIN>
+__device__ __forceinline__ void stage_x(const MgArgs& a, uint4* xs, int64_t cstride, float* red) {
+  const int tid = threadIdx.x, K = a.K;
+  uint32_t* xw = reinterpret_cast<uint32_t*>(xs);
+  if constexpr (XIN == MG_X_BF16) {
+    const int kp = K / 2;
+    for (int i = tid; i < a.nb * kp; i += kThreads) {
+      const int n = i / kp, k = 2 * (i - n * kp);
+      xw[frag_u32(n, k, cstride)] = *reinterpret_cast<const uint32_t*>(a.xb + (int64_t)n * a.xb_stride + k);
+    }
+  } else {  // MG_X_NORM: RMSNorm of fp32 rows (K <= 8192: at most 8 float4 per thread)
+    constexpr int MAXV = 8;
+    const int nv = K / 4;
+    for (int n = 0; n < a.nb; ++n) {
+      const float4* xr = reinterpret_cast<const float4*>(a.x_f32 + (int64_t)n * a.x_f32_stride);
+      float4 v[MAXV];
+      float ss = 0.f;
+#pragma unroll
+      for (int e = 0; e < MAXV; ++e) {
+        const int i = tid + e * kThreads;
+        v[e] = i < nv ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        ss += v[e].x * v[e].x + v[e].y * v[e].y + v[e].z * v[e].z + v[e].w * v[e].w;
+      }
+      const float tot = block_sum(ss, red);
+      const float scale = rsqrtf(tot / (float)K + a.eps);
+#pragma unroll
+      for (int e = 0; e < MAXV; ++e) {
+        const int i = tid + e * kThreads;
+        if (i < nv) {
+          const float4 w = a.norm_w ? reinterpret_cast<const float4*>(a.norm_w)[i] : make_float4(1.f, 1.f, 1.f, 1.f);
+          const __nv_bfloat162 p0 = __floats2bfloat162_rn(v[e].x * scale * w.x, v[e].y * scale * w.y);
+          const __nv_bfloat162 p1 = __floats2bfloat162_rn(v[e].z * scale * w.z, v[e].w * scale * w.w);
+          xw[frag_u32(n, 4 * i, cstride)] = *reinterpret_cast<const uint32_t*>(&p0);
+          xw[frag_u32(n, 4 * i + 2, cstride)] = *reinterpret_cast<const uint32_t*>(&p1);
+        }
+      }
+    }
+  }
+  __syncthreads();
+}
+
+// Last piece (warp range) holding tile t: pieces p own [p*T/P, (p+1)*T/P).
+__device__ __forceinline__ int64_t owner(int64_t t, int64_t T, int64_t P) { return ((t + 1) * P - 1) / T; }
+
+template <int FMT, int NB, int XIN, int EPI>
+__global__ void __launch_bounds__(kThreads, 2) mg_gemv_kernel(MgArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  constexpr int TB = Tile<FMT>::BYTES;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint8_t* ring = smem + warp * kStages * TB;
+  float2* scs = reinterpret_cast<float2*>(smem + kWarps * kStages * TB + warp * kScaleBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kWarps * (kStages * TB + kScaleBytes)) + warp * kStages;
+  float* red = reinterpret_cast<float*>(smem + kWarps * (kStages * TB + kScaleBytes) + kWarps * kStages * 8);
+  uint4* xs = reinterpret_cast<uint4*>(smem + kWarps * (kStages * TB + kScaleBytes) + kWarps * kStages * 8 + 128);
+
+  const int64_t T = (int64_t)a.G * a.KT;
+  const int64_t P = (int64_t)gridDim.x * kWarps;
+  const int64_t p = (int64_t)blockIdx.x * kWarps + warp;
+  const int64_t t0 = p * T / P, t1 = (p + 1) * T / P;
+  const int n_tiles = (int)(t1 - t0);
+
+  if (lane == 0) {
+    for (int s = 0; s < kStages; ++s) sm100::mbar_init(&bars[s], 1);
+    sm100::fence_barrier_init();
+  }
+  __syncwarp();
+  auto issue = [&](int i) {
+    const int st = i % kStages;
+    sm100::mbar_arrive_expect_tx(&bars[st], TB);
+    sm100::bulk_g2s(ring + st * TB, a.tiles + (t0 + i) * (int64_t)TB, TB, &bars[st]);
+  };
+  // weights first: they do not depend on the previous kernel
+  int issued = n_tiles < kStages ? n_tiles : kStages;  // same value on every lane
+  if (lane == 0)
+    for (int k = 0; k < issued; ++k) issue(k);
+  pdl_launch();
+  pdl_wait();
+
+  XFrag x;
+  if constexpr (XIN == MG_X_FRAG) {
+    x.p = a.xfrag;
+    x.cstride = a.xfrag_cstride;
+  } else {
+    const int64_t cs = (int64_t)a.K / 64 * 8 + 1;  // one spare uint4 per column: bank spread
+    stage_x<XIN>(a, xs, cs, red);
+    x.p = xs;
+    x.cstride = cs;
+  }
+
+  float sum[4] = {0.f, 0.f, 0.f, 0.f};
+  int i = 0;
+  bool ok = true;
+  for (; i < n_tiles; ++i) {
+    const int st = i % kStages;
+    if (!sm100::mbar_wait(&bars[st], (uint32_t)((i / kStages) & 1), a.status)) {
+      ok = false;
+      break;
+    }
+    const int64_t ti = t0 + i;
+    const int64_t g = ti / a.KT;
+    const int s = (int)(ti - g * a.KT);
+    consume_q4k<NB>(ring + st * TB, s, x, scs, lane, sum);  // ends with __syncwarp: the stage is free
+    if (i + kStages < n_tiles) {
+      if (lane == 0) {
+        sm100::fence_proxy_async_smem();  // this stage's generic reads before the async overwrite
+        issue(i + kStages);
+      }
+      issued = i + kStages + 1;
+    }
+    const bool last = (i == n_tiles - 1) || ((ti + 1) / a.KT != g);
+    if (!last) continue;
+    // row group g done for this warp: direct epilogue, or partial + deterministic fix-up
+    const int64_t pf = owner(g * a.KT, T, P), pl = owner(g * a.KT + a.KT - 1, T, P);
+    if (pf == pl) {
+      epilogue<EPI>(a, g, sum, lane);
+    } else {
+      const int slot = (t0 / a.KT == g) ? 0 : 1;
+      __stcg(a.part + (p * 2 + slot) * 32 + lane, make_float4(sum[0], sum[1], sum[2], sum[3]));
+      __threadfence();
+      int old = 0;
+      if (lane == 0) old = atomicAdd(a.counters + g, 1);
+      old = __shfl_sync(0xffffffffu, old, 0);
+      if (old == (int)(pl - pf)) {
+        __threadfence();
+        float v[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int64_t pp = pf; pp <= pl; ++pp) {
+          const int sl = ((pp * T / P) / a.KT == g) ? 0 : 1;
+          const float4 pv = __ldcg(a.part + (pp * 2 + sl) * 32 + lane);
+          v[0] += pv.x;
+          v[1] += pv.y;
+          v[2] += pv.z;
+          v[3] += pv.w;
+        }
+        if (lane == 0) a.counters[g] = 0;
+        epilogue<EPI>(a, g, v, lane);
+      }
+    }
+    sum[0] = sum[1] = sum[2] = sum[3] = 0.f;
+  }
+  if (!ok && lane == 0) {
+    // wait (bounded) for this warp's copies still in flight before the CTA may exit
+    for (int k = i; k < issued; ++k) sm100::mbar_wait(&bars[k % kStages], (uint32_t)((k / kStages) & 1), nullptr, 1u << 22);
+  }
+}
+
+size_t smem_bytes(int fmt, int xin, int nb, int K) {
+  const size_t tb = (size_t)mg_tile_bytes(fmt);
+  size_t s = kWarps * (kStages * tb + kScaleBytes) + kWarps * kStages * 8 + 128;
+  if (xin != MG_X_FRAG) s += (size_t)nb * ((size_t)K / 64 * 8 + 1) * 16;
+  return s;
+}
+
+template <int FMT, int XIN, int EPI>
+void dispatch_nb(const MgArgs& a, int grid, cudaStream_t st, bool pdl) {
+  const size_t smem = smem_bytes(FMT, XIN, a.nb, a.K);
+  auto go = [&](auto kern) {
+    HK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    launch(kern, dim3(grid), dim3(kThreads), smem, st, pdl, a);
+  };
+  if (a.nb == 1) go(mg_gemv_kernel<FMT, 1, XIN, EPI>);
+  else if (a.nb == 2) go(mg_gemv_kernel<FMT, 2, XIN, EPI>);
+  else if (a.nb <= 4) go(mg_gemv_kernel<FMT, 4, XIN, EPI>);
+  else go(mg_gemv_kernel<FMT, 8, XIN, EPI>);
+}
+
+template <int FMT, int XIN>
+void dispatch_epi(int epi, const MgArgs& a, int grid, cudaStream_t st, bool pdl) {
+  switch (epi) {
+    case MG_STORE: dispatch_nb<FMT, XIN, MG_STORE>(a, grid, st, pdl); break;
+    case MG_RESID: dispatch_nb<FMT, XIN, MG_RESID>(a, grid, st, pdl); break;
+    case MG_SWIGLU: dispatch_nb<FMT, XIN, MG_SWIGLU>(a, grid, st, pdl); break;
+    case MG_PUSH: dispatch_nb<FMT, XIN, MG_PUSH>(a, grid, st, pdl); break;
+    default: throw std::runtime_error("mg_gemv: bad epilogue");
+  }
+}
+
+// ---- packing: GGUF Q4_K planes -> fragment-ordered tiles ------------------------------------
+__global__ void pack_q4k_kernel(const uint8_t* qs, int64_t rb0, const uint8_t* hdr, int64_t rb1, const int* rowmap,
+                                int G, int KT, uint32_t* out) {
+  const int64_t total = (int64_t)G * KT * 576;  // 32-bit words per tile: 64 header + 512 quant
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t tile = idx / 576;
+    const int w = (int)(idx - tile * 576);
+    const int64_t g = tile / KT;
+    const int s = (int)(tile - g * KT);
+    if (w < 64) {
+      const int src = rowmap[g * 16 + (w >> 2)];
+      out[idx] = src < 0 ? 0u
+                         : *reinterpret_cast<const uint32_t*>(hdr + (int64_t)src * rb1 + (int64_t)s * 16 + (w & 3) * 4);
+      continue;
+    }
+    const int qw = w - 64;  // ((ks >> 2) * 32 + t) * 4 + (ks & 3)
+    const int t = (qw >> 2) & 31, ks = (qw >> 7) * 4 + (qw & 3);
+    const int r0 = t >> 2, q = t & 3, e0 = 16 * ks + 2 * q;
+    const int s0 = rowmap[g * 16 + r0], s1 = rowmap[g * 16 + r0 + 8];
+    auto nib = [&](int src, int e) -> uint32_t {
+      if (src < 0) return 0u;
+      const uint8_t b = qs[(int64_t)src * rb0 + (int64_t)s * 128 + 32 * (e >> 6) + (e & 31)];
+      return (e & 32) ? (uint32_t)(b >> 4) : (uint32_t)(b & 15);
+    };
+    out[idx] = nib(s0, e0) | nib(s0, e0 + 1) << 16 | nib(s1, e0) << 4 | nib(s1, e0 + 1) << 20 | nib(s0, e0 + 8) << 8 |
+               nib(s0, e0 + 9) << 24 | nib(s1, e0 + 8) << 12 | nib(s1, e0 + 9) << 28;
+  }
+}
+
+}  // namespace mg
+
+int mg_tile_bytes(int fmt) {
+  switch (fmt) {
+    case WF_Q4_K: return mg::Tile<WF_Q4_K>::BYTES;
+    default: return 0;
+  }
+}
+
+size_t mg_smem_bytes(int fmt, int xin, int nb, int K) { return mg::smem_bytes(fmt, xin, nb, K); }
+
+void mg_pack_launch(int fmt, const WPlanes& w, const int* rowmap, int G, int KT, uint8_t* out, cudaStream_t s) {
+  if (fmt != WF_Q4_K) throw std::runtime_error("mg_pack: format not supported by the W4A16 GEMV");
+  const int64_t total = (int64_t)G * KT * 576;
+  const int threads = 256;
+  const int blocks = (int)std::min<int64_t>((total + threads - 1) / threads, 65536);
+  mg::pack_q4k_kernel<<<blocks, threads, 0, s>>>(w.p0, w.rb0, w.p1, w.rb1, rowmap, G, KT,
+                                                 reinterpret_cast<uint32_t*>(out));
+  HK_CUDA_CHECK(cudaGetLastError());
+}
+
+void mg_gemv_launch(int fmt, int xin, int epi, const MgArgs& a, int grid, cudaStream_t s, bool pdl) {
+  if (fmt != WF_Q4_K) throw std::runtime_error("mg_gemv: format not supported");
+  if (a.nb < 1 || a.nb > 8) throw std::runtime_error("mg_gemv: batch columns must be 1..8");
+  if (a.K % 256) throw std::runtime_error("mg_gemv: K must be a multiple of 256");
+  if (xin == MG_X_NORM && a.K > 8192) throw std::runtime_error("mg_gemv: fused RMSNorm input needs K <= 8192");
+  if (xin != MG_X_FRAG && mg::smem_bytes(fmt, xin, a.nb, a.K) > 220 * 1024)
+    throw std::runtime_error("mg_gemv: activations too wide to stage in shared memory (use the fragment input)");
+  if (epi == MG_SWIGLU && !a.hfrag && !a.hb) throw std::runtime_error("mg_gemv swiglu: output buffer required");
+  if ((epi == MG_STORE || epi == MG_RESID) && !a.y) throw std::runtime_error("mg_gemv: output y required");
+  if (epi == MG_PUSH && (!a.push_recv || !a.push_epoch || a.push_n <= 0))
+    throw std::runtime_error("mg_gemv push: peer tables required");
+  if (!a.part || !a.counters) throw std::runtime_error("mg_gemv: scratch required");
+  switch (xin) {
+    case MG_X_NORM: mg::dispatch_epi<WF_Q4_K, MG_X_NORM>(epi, a, grid, s, pdl); break;
+    case MG_X_BF16: mg::dispatch_epi<WF_Q4_K, MG_X_BF16>(epi, a, grid, s, pdl); break;
+    case MG_X_FRAG: mg::dispatch_epi<WF_Q4_K, MG_X_FRAG>(epi, a, grid, s, pdl); break;
+    default: throw std::runtime_error("mg_gemv: bad input mode");
+  }
+}
+
+}  // namespace hk

@@ -1,0 +1,173 @@
+"""Full-precision small-batch GEMV (W4A16) on the tensor cores: Python surface of mma_gemv.cu.
+
+``MgWeight`` is a Q4_K matrix re-laid once into fragment-ordered tiles of 16 rows x 256 columns
+(a lossless permutation of the GGUF bytes: the 16-byte super-block headers are copied unchanged and
+the quant nibbles are reordered). ``pack(w)`` keeps row order; ``pack(w_gate_up, swiglu=F)``
+interleaves the gate and up halves of a fused [gate | up] matrix 8 + 8 rows per tile so the
+SwiGLU product can be formed in the GEMV epilogue.
+
+Inputs: ``x_norm`` (fp32 rows + RMSNorm weight, normalised inside the kernel), ``xb`` (bf16 rows)
+or ``xfrag`` (a ``FragAct``: bf16 already in the tensor-core fragment order, as written by the
+SwiGLU epilogue). Outputs: fp32 rows (store or residual add), SwiGLU h (``FragAct`` and/or bf16
+rows), or the tensor-parallel push.
+
+Parity: crates/hawking-core/shaders/quant.metal gemm_q4_k_m_fused* (fp32 activations; the W4A8
+variant is off by default in the reference, workspace/docs/reference/env_flags.md:38).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Dict, Optional
+
+import torch
+
+from .._ext import kernels
+from ..formats.ggml import GgmlType
+from .qweight import QWeight
+
+MG_X_NORM, MG_X_BF16, MG_X_FRAG = 0, 1, 2
+MG_STORE, MG_RESID, MG_SWIGLU, MG_PUSH = 0, 1, 2, 3
+MG_FORMATS = (GgmlType.Q4_K,)
+
+
+@dataclass
+class MgWeight:
+    tiles: torch.Tensor
+    fmt: int
+    N: int          # logical output rows (SwiGLU: h rows F)
+    K: int
+    G: int          # row groups of 16 tile rows
+    KT: int         # 256-column tiles per row group
+    swiglu: bool = False
+
+    @property
+    def nbytes(self) -> int:
+        return self.tiles.numel()
+
+
+def supported(w: Optional[QWeight]) -> bool:
+    return w is not None and w.fmt in MG_FORMATS and w.K % 256 == 0
+
+
+def pack(w: QWeight, swiglu: Optional[int] = None) -> MgWeight:
+    """Re-lay ``w`` (Q4_K) into fragment-ordered tiles. ``swiglu=F``: w is [gate (F rows) | up
+    (F rows)] and tile g holds gate rows 8g..8g+7 followed by the matching up rows."""
+    if not supported(w):
+        raise ValueError(f"mg.pack: format {w.fmt} / K {w.K} not supported by the W4A16 GEMV")
+    dev = w.device
+    if swiglu:
+        F = int(swiglu)
+        if w.N != 2 * F:
+            raise ValueError("mg.pack: swiglu expects a fused [gate | up] matrix of 2F rows")
+        G = (F + 7) // 8
+        o = torch.arange(G * 8, dtype=torch.int64).view(G, 8)
+        gate = torch.where(o < F, o, torch.full_like(o, -1))
+        up = torch.where(o < F, o + F, torch.full_like(o, -1))
+        rowmap = torch.cat([gate, up], 1).reshape(-1)
+        N = F
+    else:
+        G = (w.N + 15) // 16
+        r = torch.arange(G * 16, dtype=torch.int64)
+        rowmap = torch.where(r < w.N, r, torch.full_like(r, -1))
+        N = w.N
+    KT = w.K // 256
+    tiles = torch.empty(G * KT * kernels().mg_tile_bytes(int(w.fmt)), dtype=torch.uint8, device=dev)
+    kernels().mg_pack(int(w.fmt), w.planes, rowmap.to(torch.int32).to(dev), G, KT, tiles)
+    return MgWeight(tiles, int(w.fmt), N, w.K, G, KT, bool(swiglu))
+
+
+def frag_index(K: int, nb: int, cstride: int, device) -> torch.Tensor:
+    """Flat bf16 index of x[n][k] in the B-fragment order, for n < nb, k < K (row-major [nb, K])."""
+    k = torch.arange(K, device=device)
+    ks, kk = k // 16, k % 16
+    q, reg, half = (kk % 8) // 2, kk // 8, kk % 2
+    u4 = ((ks // 4) * 4 + q) * 2 + (ks % 4) // 2
+    u32 = u4 * 4 + (ks % 2) * 2 + reg
+    col = torch.arange(nb, device=device)[:, None] * (cstride * 8)
+    return (col + (u32 * 2 + half)[None, :]).reshape(-1)
+
+
+class FragAct:
+    """bf16 activations of up to 8 columns in the tensor-core B-fragment order (K % 64 == 0)."""
+
+    def __init__(self, K: int, device, cols: int = 8):
+        if K % 64:
+            raise ValueError("FragAct: K must be a multiple of 64")
+        self.K = K
+        self.buf = torch.zeros(cols, K, dtype=torch.bfloat16, device=device)
+        self.cstride = K // 8  # uint4s per column (K bf16 = 2K bytes)
+
+    def to_plain(self, nb: int) -> torch.Tensor:
+        """[nb, K] bf16 in natural order (test helper)."""
+        return self.buf.reshape(-1)[frag_index(self.K, nb, self.cstride, self.buf.device)].view(nb, self.K)
+
+
+class MgScratch:
+    """Per-device partial-sum scratch and row-group counters shared by consecutive GEMV launches
+    (each launch writes scratch only after the previous kernel has completed, and leaves every
+    counter at zero)."""
+
+    _cache: Dict[int, "MgScratch"] = {}
+
+    def __init__(self, device, max_groups: int = 1 << 16):
+        dev = torch.device(device)
+        sms = kernels().mg_num_sms(dev.index or 0)
+        self.part = torch.zeros(sms * 8 * 2 * 32 * 4, dtype=torch.float32, device=dev)
+        self.counters = torch.zeros(max_groups, dtype=torch.int32, device=dev)
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    @classmethod
+    def get(cls, device) -> "MgScratch":
+        dev = torch.device(device)
+        if dev.index is None:
+            dev = torch.device("cuda", torch.cuda.current_device())
+        s = cls._cache.get(dev.index)
+        if s is None:
+            s = cls._cache[dev.index] = MgScratch(dev)
+        return s
+
+    def reset(self):
+        """Clear counters and status (after a failed step left a row group half counted)."""
+        self.counters.zero_()
+        self.status.zero_()
+
+
+def gemv(mw: MgWeight, nb: int, *, x_norm=None, xb: Optional[torch.Tensor] = None,
+         xfrag: Optional[FragAct] = None, y: Optional[torch.Tensor] = None, residual: bool = False,
+         bias=None, hfrag: Optional[FragAct] = None, hb: Optional[torch.Tensor] = None, argmax_slots=None,
+         argmax_offset: int = 0, push=None, status: Optional[torch.Tensor] = None, pdl: Optional[bool] = None,
+         scratch: Optional[MgScratch] = None):
+    """One W4A16 GEMV launch over ``nb`` batch columns.
+
+    ``x_norm=(x_f32, norm_w, eps)`` (norm_w may be None), ``xb`` or ``xfrag`` selects the input.
+    ``y`` with ``residual`` selects store / add; a SwiGLU-packed weight writes ``hfrag`` / ``hb``;
+    ``push=(recv_table, epoch)`` selects the tensor-parallel push.
+    """
+    from . import PDL, launches
+    sc = scratch or MgScratch.get(mw.tiles.device)
+    if x_norm is not None:
+        xin = MG_X_NORM
+    elif xb is not None:
+        xin = MG_X_BF16
+    elif xfrag is not None:
+        xin = MG_X_FRAG
+    else:
+        raise ValueError("mg.gemv: an input is required")
+    if mw.swiglu:
+        epi = MG_SWIGLU
+    elif push is not None:
+        epi = MG_PUSH
+    else:
+        epi = MG_RESID if residual else MG_STORE
+    xf, nw, eps = (x_norm if x_norm is not None else (None, None, 1e-5))
+    launches.add()
+    kernels().mg_gemv(
+        mw.fmt, xin, epi, mw.tiles, mw.G, mw.KT, mw.N, mw.K, nb,
+        x_f32=xf, norm_w=nw, eps=float(eps), xb=xb,
+        xfrag=xfrag.buf if xfrag is not None else None, xfrag_cstride=xfrag.cstride if xfrag is not None else 0,
+        y=y, bias=bias, F=mw.N if mw.swiglu else 0,
+        hfrag=hfrag.buf if hfrag is not None else None, hfrag_cstride=hfrag.cstride if hfrag is not None else 0,
+        hb=hb, argmax_slots=argmax_slots, argmax_offset=argmax_offset,
+        push_recv=push[0] if push is not None else None, push_epoch=push[1] if push is not None else None,
+        part=sc.part, counters=sc.counters, status=status if status is not None else sc.status,
+        pdl=PDL if pdl is None else pdl)
