@@ -52,6 +52,10 @@ def parse():
     ap.add_argument("--profile-step", action="store_true",
                     help="run one eager decode step between cudaProfilerStart/Stop (for ncu --profile-from-start off) "
                          "and exit without a result line")
+    ap.add_argument("--w4a8", type=int, default=1,
+                    help="also time bs1 decode with the opt-in int8-activation GEMV (reported under its own key)")
+    ap.add_argument("--repeats", type=int, default=3,
+                    help="extra blocks of K timed steps after the first (median and spread reported beside it)")
     ap.add_argument("--tp-shard-of", type=int, default=0,
                     help="one GPU runs rank 0's shard of an N-way tensor-parallel model with its collectives looped "
                          "back to itself (profiling the shard's kernels under a single-process profiler; not a result)")
@@ -64,8 +68,8 @@ def parse():
 def reference_unavailable(args):
     line = {"impl": "reference",
             "unavailable": "the reference (joshuahickscorp/hawking) is a Rust+Metal workspace with no Python "
-                           "package; pip install of /root/reference fails (no setup.py/pyproject.toml) and Metal "
-                           "does not exist on this box"}
+                           "package; pip install of the reference source tree fails (no setup.py/pyproject.toml) and "
+                           "Metal does not exist on this box"}
     print(json.dumps(line))
 
 
@@ -539,27 +543,33 @@ def main():
         m.inp.upload(ids, pos, [0] * nseq, rseq, rctx)
         return [first_id + i for i in range(nseq)]
 
-    def timed_decode(nseq):
+    def timed_decode(nseq, repeats=0):
+        """W warm-up steps, then the timed block of exactly K steps (barrier + synchronize on both
+        sides, CUDA events, max over ranks); then ``repeats`` more blocks of K steps, reported
+        separately. Clocks are sampled across all blocks."""
         for _ in range(W):
             m.graph_forward(nseq, "greedy", advance=True)
         torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        blocks = []
         with ClockSampler(local, period_ms=50) as cs:
-            # the barrier comes after every rank's sampler is up, so all ranks start together
-            barrier()
-            torch.cuda.synchronize()
-            e0.record()
-            for _ in range(K):
-                m.graph_forward(nseq, "greedy", advance=True)
-            e1.record()
-            torch.cuda.synchronize()
-        barrier()
-        ms = e0.elapsed_time(e1) / K
-        if world > 1:
-            t = torch.tensor([ms], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = t.item()
-        return ms, cs.result
+            for _b in range(1 + repeats):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                # the barrier comes after every rank's sampler is up, so all ranks start together
+                barrier()
+                torch.cuda.synchronize()
+                e0.record()
+                for _ in range(K):
+                    m.graph_forward(nseq, "greedy", advance=True)
+                e1.record()
+                torch.cuda.synchronize()
+                barrier()
+                ms = e0.elapsed_time(e1) / K
+                if world > 1:
+                    t = torch.tensor([ms], device=dev)
+                    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                    ms = t.item()
+                blocks.append(ms)
+        return blocks[0], cs.result, blocks[1:]
 
     # Random KV content for the context (decode work does not depend on the values).
     g = torch.Generator(device=dev).manual_seed(1)
@@ -593,10 +603,24 @@ def main():
         torch.cuda.cudart().cudaProfilerStop()
         print(json.dumps({"profile_step": True, "launches": m.launches_per_forward}))
         return 0
-    ms1, clocks = timed_decode(B)
+    ms1, clocks, rep1 = timed_decode(B, args.repeats)
     launches = m.launches_per_graph
     for s in seqs:
         kv.drop(s)
+    result_w4a8 = None
+    if args.w4a8 and m.small_batch == "w4a16":
+        # the opt-in int8-activation GEMV, same workload, reported under its own key
+        m.release_graphs()
+        m.small_batch = "w4a8"
+        seqs = setup_decode(B, 3_000_000)
+        ms8a, clocks8a, _ = timed_decode(B)
+        result_w4a8 = {"tok_s": round(B * 1000.0 / ms8a, 2), "ms_per_step": round(ms8a, 4), "clocks": clocks8a,
+                       "dtype": "q4_k weights x int8 activation blocks of 32 (dp4a), fp32 accumulate (opt-in: "
+                                "HK_SMALL_BATCH=w4a8)"}
+        for s in seqs:
+            kv.drop(s)
+        m.release_graphs()
+        m.small_batch = "w4a16"
     result_bs64 = None
     if args.bs64 and B != 64 and m.row_limit < 64:
         # tensor parallel without the tensor-core path (MoE layers): the push all-reduce sites
@@ -605,7 +629,7 @@ def main():
                                       "which MoE layers do not have yet (forwards of <= 8 rows only)"}
     elif args.bs64 and B != 64:
         seqs = setup_decode(64, 2_000_000)
-        ms64, clocks64 = timed_decode(64)
+        ms64, clocks64, _ = timed_decode(64)
         result_bs64 = {"tok_s_aggregate": round(64 * 1000.0 / ms64 * replicas, 1), "ms_per_step": round(ms64, 4),
                        "clocks": clocks64}
         for s in seqs:
@@ -661,9 +685,11 @@ def main():
         "warmup": W,
         "ms_per_step": round(ms1, 4),
         "higher_is_better": True,
-        "scaling": "strong" if use_tp else "weak",
+        "scaling": "strong" if args.parallel == "tp" else "weak",
         "vs_baseline": None,
-        "dtype": "q4_k weights, int8 activation blocks (W4A8 dp4a), fp32 accumulate, bf16 KV",
+        "dtype": ("q4_k weights, bf16 activations (W4A16 tensor-core GEMV), fp32 accumulate, bf16 KV"
+                  if m.small_batch == "w4a16" else
+                  "q4_k weights, int8 activation blocks (W4A8 dp4a), fp32 accumulate, bf16 KV"),
         "data": "synthetic: random-init N(0,0.02) weights quantised to GGUF Q4_K on device; uniform-random "
                 "token ids; device-timed decode runs over a 2048-token KV context filled with random bf16",
         "config": {"model": "llama3-8b (Llama-3-8B-arch: 32 layers, hidden 4096, 32/8 GQA heads, head_dim 128, "
@@ -677,6 +703,8 @@ def main():
         "e2e": e2e,
         "gpu_launches": launches * K,
         "bs64": result_bs64,
+        "repeat_blocks_ms_per_step": [round(v, 4) for v in rep1],
+        "w4a8_opt_in": result_w4a8,
         "ttft_p50_ms": round(ttft_p50, 2),
         "ttft_runs_ms": [round(t, 2) for t in ttfts],
         "weights_gb": round(w.nbytes / 1e9, 3),
@@ -687,8 +715,8 @@ def main():
         out["invalid"] = f"one GPU ran rank 0's shard of a {args.tp_shard_of}-way TP model, collectives looped back"
     if tp is not None:
         tp.check()
-        out["tp_collectives"] = "decode: GEMV epilogue pushes partials over NVLink + fused all-reduce/RMSNorm; " \
-                                "prefill and bs64 (tensor-core path): NCCL all-reduce"
+        out["tp_collectives"] = "decode (<= 8 rows): GEMV epilogue pushes partials over NVLink + fused " \
+                                "all-reduce/RMSNorm; prefill and bs64 (tensor-core path): NCCL all-reduce"
     if rank == 0:
         print(json.dumps(out))
     if world > 1:

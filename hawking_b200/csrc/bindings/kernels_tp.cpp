@@ -58,8 +58,9 @@ void tp_begin(const Tensor& epoch, bool pdl) {
 
 void tp_allreduce_rmsnorm_q8(const Tensor& x_in, const Tensor& x_out, int64_t recv, int64_t rank_stride, int64_t n,
                              const Tensor& epoch, const c10::optional<Tensor>& w,
-                             double eps, const Tensor& xq, const Tensor& xd, const Tensor& xs, const Tensor& status,
-                             bool pdl) {
+                             double eps, const c10::optional<Tensor>& xq, const c10::optional<Tensor>& xd,
+                             const c10::optional<Tensor>& xs, const Tensor& status, bool pdl,
+                             const c10::optional<Tensor>& yb, int64_t wait_ns) {
   TORCH_CHECK(x_in.is_cuda() && x_in.scalar_type() == at::kFloat && x_out.scalar_type() == at::kFloat,
               "tp norm: fp32 residual rows");
   TORCH_CHECK(x_in.stride(0) == x_out.stride(0), "tp norm: x_in / x_out strides differ");
@@ -74,16 +75,25 @@ void tp_allreduce_rmsnorm_q8(const Tensor& x_in, const Tensor& x_out, int64_t re
   a.w = w.has_value() ? w->data_ptr<float>() : nullptr;
   a.eps = (float)eps;
   a.K = (int)x_in.size(1);
-  a.xq = xq.data_ptr<int8_t>();
-  a.xd = xd.data_ptr<float>();
-  a.xs = xs.data_ptr<float>();
+  if (xq.has_value()) {
+    TORCH_CHECK(xd.has_value() && xs.has_value(), "tp norm: q8 output needs q, d and s");
+    a.xq = xq->data_ptr<int8_t>();
+    a.xd = xd->data_ptr<float>();
+    a.xs = xs->data_ptr<float>();
+  } else {
+    TORCH_CHECK(yb.has_value() && yb->scalar_type() == at::kBFloat16 && yb->stride(-1) == 1,
+                "tp norm: a q8 or a bf16 output is required");
+    a.yb = reinterpret_cast<__nv_bfloat16*>(yb->data_ptr());
+    a.yb_stride = yb->stride(0);
+  }
   a.status = status.data_ptr<int>();
+  a.wait_ns = (unsigned long long)(wait_ns > 0 ? wait_ns : 0);
   const c10::cuda::CUDAGuard g(x_in.device());
   hk::tp_allreduce_rmsnorm_q8_launch(a, (int)x_in.size(0), cur_stream(), pdl);
 }
 
 void tp_argmax(const Tensor& slots, int64_t rows, int64_t max_rows, const Tensor& keys_table, int64_t keys_local,
-               const Tensor& uses, int64_t me, const Tensor& out, const Tensor& status, bool pdl) {
+               const Tensor& uses, int64_t me, const Tensor& out, const Tensor& status, bool pdl, int64_t wait_ns) {
   TORCH_CHECK(slots.is_cuda() && slots.scalar_type() == at::kLong, "tp_argmax: int64 slots");
   TORCH_CHECK(keys_table.scalar_type() == at::kLong, "tp_argmax: int64 pointer table");
   TORCH_CHECK(rows <= max_rows, "tp_argmax: rows exceed the key region");
@@ -98,6 +108,7 @@ void tp_argmax(const Tensor& slots, int64_t rows, int64_t max_rows, const Tensor
   a.n = (int)keys_table.numel();
   a.out = out.data_ptr<int>();
   a.status = status.data_ptr<int>();
+  a.wait_ns = (unsigned long long)(wait_ns > 0 ? wait_ns : 0);
   const c10::cuda::CUDAGuard g(slots.device());
   hk::tp_argmax_launch(a, cur_stream(), pdl);
 }
@@ -113,8 +124,9 @@ void register_tp_kernels(py::module_& m) {
   m.def("tp_begin", &tp_begin, py::arg("epoch"), py::arg("pdl") = false);
   m.def("tp_allreduce_rmsnorm_q8", &tp_allreduce_rmsnorm_q8, py::arg("x_in"), py::arg("x_out"), py::arg("recv"),
         py::arg("rank_stride"), py::arg("n"), py::arg("epoch"), py::arg("w"), py::arg("eps"), py::arg("xq"), py::arg("xd"), py::arg("xs"), py::arg("status"),
-        py::arg("pdl") = false);
+        py::arg("pdl") = false, py::arg("yb") = py::none(), py::arg("wait_ns") = 0);
   m.def("tp_argmax", &tp_argmax, py::arg("slots"), py::arg("rows"), py::arg("max_rows"), py::arg("keys_table"),
-        py::arg("keys_local"), py::arg("uses"), py::arg("me"), py::arg("out"), py::arg("status"), py::arg("pdl") = false);
+        py::arg("keys_local"), py::arg("uses"), py::arg("me"), py::arg("out"), py::arg("status"), py::arg("pdl") = false,
+        py::arg("wait_ns") = 0);
 }
 }  // namespace hk

@@ -83,10 +83,13 @@ struct TpReduceArgs {
   const float* w;               // RMSNorm weight of the next projection
   float eps;
   int K;
-  int8_t* xq;
+  int8_t* xq;                   // q8 output of the normalised rows, or null:
   float* xd;
   float* xs;
+  __nv_bfloat16* yb;            //   bf16 normalised rows [rows, yb_stride] (W4A16 consumers)
+  int64_t yb_stride;
   int* status;
+  unsigned long long wait_ns;   // bound of each peer wait (0: the default, one second)
 };
 struct TpArgmaxArgs {
   unsigned long long* slots;    // local fused-argmax slots [rows, kArgmaxSlots] (cleared here)
@@ -97,6 +100,7 @@ struct TpArgmaxArgs {
   int me, n;
   int* out;                     // token ids [rows]
   int* status;
+  unsigned long long wait_ns;   // bound of each peer wait (0: the default, one second)
 };
 void tp_begin_launch(int* epoch, cudaStream_t s, bool pdl);
 void tp_allreduce_rmsnorm_q8_launch(const TpReduceArgs& a, int rows, cudaStream_t s, bool pdl);

@@ -617,6 +617,7 @@ void attention_decode_launch(const AttnDecodeArgs& a, cudaStream_t s, bool pdl) 
   if (a.nh % a.nkv) throw std::runtime_error("attention: n_heads must be a multiple of n_kv_heads");
   if (a.num_splits > 64) throw std::runtime_error("attention: at most 64 splits");
   if (a.num_splits > 1 && !a.counters) throw std::runtime_error("attention: split-KV needs the counter scratch");
+  if (a.block_size < 8) throw std::runtime_error("attention: block_size must be at least 8");
   const int G = a.nh / a.nkv;
   switch (a.hd) {
     case 64: launch_hpl<2>(a, G, s, pdl); break;
@@ -629,30 +630,18 @@ void attention_decode_launch(const AttnDecodeArgs& a, cudaStream_t s, bool pdl) 
 }  // namespace hk
 
 // =================================================================================================
-// Allocation-free entry point: hk_attention_decode_noalloc
+// Allocation-free entry point: hk_attention_decode_noalloc (declared, with its limits and the
+// rules for callers, in noalloc.h). No counterpart in the reference.
 //
-// No counterpart in the reference (its Metal engine has no C entry points of this kind).
-//
-// Some callers of this library cannot call cudaMalloc: an engine embedded in a host process whose
-// own allocator has already reserved the device memory, or a latency-critical decode loop where
-// cudaMalloc/cudaFree (which may synchronise the device) are not allowed. This entry point runs
-// the same split-KV paged decode attention as attention_decode_launch, but its scratch (the
-// per-split partial outputs, their log-sum-exps and the split counters) lives in fixed-size
-// file-scope device arrays instead of caller-provided or freshly allocated buffers. The caller
-// still passes every input and output.
-//
-// Limits: at most kNoAllocPartElems partial-output floats (rows * n_heads * num_splits * head_dim),
-// kNoAllocLseElems log-sum-exps (rows * n_heads * num_splits) and kNoAllocCounters counters
-// (rows * n_kv_heads); larger requests are rejected with HK_NOALLOC_TOO_LARGE. Every GPU that
-// loads this library holds these arrays (about 4.1 MiB) until the process exits.
-//
-// The first call on a device resolves the arrays' device addresses (cudaGetSymbolAddress, with
-// that device current); make that first call before any stream capture. Every call shares the
-// same arrays: calls that overlap on the GPU (different streams, or different host threads with
-// no ordering between their streams) race on the scratch and must not be issued concurrently.
-// The split counters are cleared at the start of every call; the partials are fully overwritten.
+// Callers that cannot call cudaMalloc (an engine embedded in a host whose allocator owns the
+// device memory, or a decode loop where allocation and its possible device synchronisation are
+// not allowed) get the same split-KV decode attention with its scratch in fixed file-scope device
+// arrays. Their device addresses are looked up once per device (cudaGetSymbolAddress with that
+// device current) on the first call, which should come before any stream capture.
 // =================================================================================================
 #include <mutex>
+
+#include "noalloc.h"
 
 namespace {
 constexpr int64_t kNoAllocPartElems = int64_t(1) << 20;  // 4 MiB of fp32 partial outputs
@@ -680,15 +669,8 @@ int noalloc_fail(int code, const std::string& msg) {
 }
 }  // namespace
 
-enum HkNoAllocStatus : int {
-  HK_NOALLOC_OK = 0,
-  HK_NOALLOC_BAD_ARG = 1,
-  HK_NOALLOC_TOO_LARGE = 2,
-  HK_NOALLOC_CUDA_ERROR = 3,
-};
-
 // Message of the last failing call on this host thread ("" after a success).
-extern "C" __attribute__((visibility("default"))) const char* hk_attention_decode_noalloc_error() {
+extern "C" __attribute__((visibility("default"))) const char* hk_attention_decode_noalloc_error(void) {
   return g_noalloc_error.c_str();
 }
 
@@ -712,6 +694,12 @@ extern "C" __attribute__((visibility("default"))) int hk_attention_decode_noallo
     return noalloc_fail(HK_NOALLOC_BAD_ARG, "invalid geometry");
   if (head_dim != 64 && head_dim != 128 && head_dim != 256)
     return noalloc_fail(HK_NOALLOC_BAD_ARG, "head_dim must be 64, 128 or 256");
+  // a tile of up to 8 consecutive tokens may span at most two KV blocks
+  if (block_size < 8) return noalloc_fail(HK_NOALLOC_BAD_ARG, "block_size must be at least 8");
+  // vector loads of K/V (up to 16 bytes per lane) and q / out rows
+  if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache) | reinterpret_cast<uintptr_t>(q) |
+       reinterpret_cast<uintptr_t>(out)) & 15)
+    return noalloc_fail(HK_NOALLOC_BAD_ARG, "q, k_cache, v_cache and out must be 16-byte aligned");
   const int64_t part = (int64_t)rows * n_heads * num_splits * head_dim;
   const int64_t lse = (int64_t)rows * n_heads * num_splits;
   const int64_t cnt = (int64_t)rows * n_kv_heads;
@@ -740,6 +728,12 @@ extern "C" __attribute__((visibility("default"))) int hk_attention_decode_noallo
     sc = s;
   }
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (st) {  // the scratch looked up above is the current device's: the stream must be on it too
+    int sdev = -1;
+    if (cudaStreamGetDevice(st, &sdev) != cudaSuccess)
+      return noalloc_fail(HK_NOALLOC_BAD_ARG, "stream is not a valid CUDA stream");
+    if (sdev != dev) return noalloc_fail(HK_NOALLOC_BAD_ARG, "stream belongs to another device than the current one");
+  }
   // The split counters must start at zero (a previous call may have been interrupted).
   cudaError_t e = cudaMemsetAsync(sc.counters, 0, sizeof(int) * cnt, st);
   if (e != cudaSuccess) return noalloc_fail(HK_NOALLOC_CUDA_ERROR, std::string("clearing counters: ") + cudaGetErrorString(e));

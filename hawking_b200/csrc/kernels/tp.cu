@@ -22,7 +22,8 @@
 // same way (two flagged words per key); every rank then reduces the N keys to the token id.
 //
 // Every wait is bounded (status word HK_ERR_PEER_TIMEOUT, then the kernel carries on with what
-// it has): a rank that stopped cannot hang the others' GPUs.
+// it has; the engine reads the status after the step and discards the step's tokens): a rank that
+// stopped cannot hang the others' GPUs. The bound is a kernel argument (default one second).
 #include <cooperative_groups.h>
 
 #include "decode_ops.cuh"
@@ -44,7 +45,8 @@ constexpr int kTpCluster = 8;   // CTAs per row (one cluster)
 constexpr int kTpMaxE = 4;      // elements per thread: K <= kTpCluster * 256 * kTpMaxE
 constexpr int kTpMaxRanks = 8;
 
-// Consumer: x_out = x_in + sum over ranks of the partials, then RMSNorm (weight w) -> q8 blocks.
+// Consumer: x_out = x_in + sum over ranks of the partials, then RMSNorm (weight w) -> q8 blocks
+// (or bf16 rows when xq is null).
 // Grid (kTpCluster, rows), clusters of kTpCluster CTAs along x; CTA c owns elements
 // [c * K / C, (c + 1) * K / C) of its row, 256 threads striding over them (a warp owns whole
 // 32-element q8 blocks).
@@ -58,7 +60,7 @@ __global__ void __cluster_dims__(kTpCluster, 1, 1) __launch_bounds__(256)
   const int r = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int K = a.K, chunk = K / kTpCluster, base = c * chunk, n = a.n;
   const uint32_t flag = (uint32_t)*a.epoch;
-  const unsigned long long deadline = global_ns() + kTpWaitNs;
+  const unsigned long long deadline = global_ns() + (a.wait_ns ? a.wait_ns : kTpWaitNs);
   const unsigned long long* rr = a.recv + (int64_t)r * K;
   const float* xr = a.x_in + (int64_t)r * a.x_stride;
 
@@ -113,6 +115,10 @@ __global__ void __cluster_dims__(kTpCluster, 1, 1) __launch_bounds__(256)
     a.x_out[(int64_t)r * a.x_stride + e] = v[j];
     float y = v[j] * scale;
     if (a.w) y *= a.w[e];
+    if (!a.xq) {  // bf16 output (uniform across the grid)
+      if (a.yb) a.yb[(int64_t)r * a.yb_stride + e] = __float2bfloat16_rn(y);
+      continue;
+    }
     const float amax = warp_max(fabsf(y));
     const float d = amax / 127.f;
     const int q = amax > 0.f ? __float2int_rn(y / d) : 0;
@@ -168,7 +174,7 @@ __global__ void __launch_bounds__(256) tp_argmax_kernel(TpArgmaxArgs a) {
     }
     __syncthreads();
   }
-  const unsigned long long deadline = global_ns() + kTpWaitNs;
+  const unsigned long long deadline = global_ns() + (a.wait_ns ? a.wait_ns : kTpWaitNs);
   bool ok = true;
   for (int r = tid; r < a.rows; r += blockDim.x) {
     unsigned long long b = 0;

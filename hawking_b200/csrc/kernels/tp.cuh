@@ -11,7 +11,7 @@
 
 namespace hk {
 
-constexpr unsigned long long kTpWaitNs = 1000000000ull;  // bounded wait: 1 s, then HK_ERR_PEER_TIMEOUT
+constexpr unsigned long long kTpWaitNs = 1000000000ull;  // default bound of a peer wait: 1 s, then HK_ERR_PEER_TIMEOUT
 
 __device__ __forceinline__ unsigned long long global_ns() {
   unsigned long long t;

@@ -31,6 +31,18 @@ from .kv_cache import PagedKVCache
 from .sampling import RequestRng, SamplingParams
 
 
+class DeviceStatusError(RuntimeError):
+    """A kernel of the step reported a failed bounded wait through a device status word
+    (1 bounds guard, 2 peer timeout, 3 mbarrier timeout, 4 bad argument)."""
+
+    NAMES = {1: "bounds guard", 2: "peer timeout", 3: "mbarrier timeout", 4: "bad argument"}
+
+    def __init__(self, codes):
+        self.codes = list(codes)
+        what = ", ".join(f"{c} ({self.NAMES.get(c, 'unknown')})" for c in self.codes if c)
+        super().__init__(f"device status word set: {what}; the step's tokens were discarded")
+
+
 @dataclass
 class RequestState:
     id: int
@@ -68,6 +80,12 @@ class Engine:
         self.use_graphs = use_graphs
         self.stats = EngineStats()
         self._host_ids = torch.zeros(model.max_rows, dtype=torch.int32).pin_memory()
+        # device status words read back after every step (model kernels' bounded waits, and the
+        # tensor-parallel collectives' peer waits): a nonzero word fails the step before any of
+        # its tokens are committed
+        self._status_dev = [t for t in (getattr(model, "status", None),
+                                        getattr(getattr(model, "tp", None), "status", None)) if t is not None]
+        self._host_status = torch.zeros(max(1, len(self._status_dev)), dtype=torch.int32).pin_memory()
         self.tokenizer = None  # token bytes for JSON-mode requests (set by the server)
         # per-step cost ledger (HK_LEDGER=1 or ledger=True): host phases of every step, in us
         self.ledger_on = (os.environ.get("HK_LEDGER", "0") == "1") if ledger is None else ledger
@@ -325,6 +343,7 @@ class Engine:
                 with trace("sample"):
                     sampled.extend(self._sample(picks, greedy))
             t_smp += time.perf_counter() - tb
+        self._check_device_status()
         if serial and sample_rows:  # back to the plan's item order (rows ran in wave order)
             by_id = {it.id: tok for (it, _), tok in zip(sample_rows, sampled)}
             sampled = [by_id[it.id] for it in items if it.id in by_id]
@@ -356,6 +375,30 @@ class Engine:
         else:
             self.stats.prefill_rows += n
         return out
+
+    def _check_device_status(self):
+        """Read every device status word of this step (one small copy, then a stream sync, which
+        the sampled ids needed anyway) and raise DeviceStatusError when a kernel reported a failed
+        bounded wait. Nothing of the step is committed then; the words stay set until
+        ``clear_device_status``."""
+        if not self._status_dev:
+            return
+        m = self.model
+        for i, t in enumerate(self._status_dev):
+            self._host_status[i:i + 1].copy_(t.view(-1)[:1], non_blocking=True)
+        torch.cuda.current_stream(m.dev).synchronize()
+        self.stats.d2h_bytes += 4 * len(self._status_dev)
+        codes = [int(v) for v in self._host_status[:len(self._status_dev)].tolist()]
+        if any(codes):
+            raise DeviceStatusError(codes)
+
+    def clear_device_status(self):
+        """Zero the status words (and the small-batch GEMV's split-K counters, which a failed
+        launch can leave half counted) after the cause was handled."""
+        for t in self._status_dev:
+            t.zero_()
+        from ..ops import mg
+        mg.MgScratch.get(self.model.dev).reset()
 
     def _sample(self, rows_here, greedy: bool) -> List[int]:
         m = self.model

@@ -18,6 +18,7 @@ token), :9131 (forward_tokens_multiseq_greedy), :9384 (forward_tokens_verify).
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass, field
 from typing import Dict, List, Optional
 
@@ -27,6 +28,7 @@ from .. import ops
 from ..formats.ggml import GgmlType, type_id
 from ..formats.gguf import GgufModel
 from ..ops import Q8Act, QWeight, cat_rows
+from ..ops import mg
 from .config import ModelConfig
 
 GEMV_COLS = 8  # rows per GEMV launch (dp4a GEMV batch limit)
@@ -46,6 +48,15 @@ class LayerWeights:
     k_norm: Optional[torch.Tensor] = None
     moe: Optional[object] = None  # MoE FFN module (models/moe.py)
     w_gu: Optional[QWeight] = None  # fused [gate | up] rows (w_gate / w_up are views of it)
+    # the same matrices re-laid for the W4A16 small-batch GEMV (ops/mg.py), when supported
+    mg_qkv: Optional[object] = None
+    mg_o: Optional[object] = None
+    mg_gu: Optional[object] = None
+    mg_down: Optional[object] = None
+
+    def mg_ready(self) -> bool:
+        return self.mg_qkv is not None and self.mg_o is not None and (
+            self.moe is not None or (self.mg_gu is not None and self.mg_down is not None))
 
     def fuse_gate_up(self):
         if self.w_gate is not None and self.w_gate.fmt == self.w_up.fmt and self.w_gu is None:
@@ -61,6 +72,32 @@ class LlamaWeights:
     lm_head: QWeight
     layers: List[LayerWeights]
     rope_freqs: Optional[torch.Tensor] = None
+    mg_head: Optional[object] = None
+
+    def prepare_mg(self):
+        """Re-lay every supported projection for the W4A16 small-batch GEMV (once; the planar
+        GGUF copy stays for the tensor-core GEMM of prefill and large batches)."""
+        for l in self.layers:
+            if l.mg_qkv is None and len(l.wqkv) == 1 and mg.supported(l.wqkv[0]):
+                l.mg_qkv = mg.pack(l.wqkv[0])
+            if l.mg_o is None and mg.supported(l.wo):
+                l.mg_o = mg.pack(l.wo)
+            if l.moe is None and l.mg_gu is None and l.w_gu is not None and mg.supported(l.w_gu) \
+                    and l.w_gu.N == 2 * l.w_down.K and l.w_down.K % 64 == 0:
+                l.mg_gu = mg.pack(l.w_gu, swiglu=l.w_down.K)
+            if l.moe is None and l.mg_down is None and mg.supported(l.w_down):
+                l.mg_down = mg.pack(l.w_down)
+        if self.mg_head is None and mg.supported(self.lm_head):
+            self.mg_head = mg.pack(self.lm_head)
+
+    @property
+    def mg_nbytes(self) -> int:
+        n = self.mg_head.nbytes if self.mg_head is not None else 0
+        for l in self.layers:
+            for m in (l.mg_qkv, l.mg_o, l.mg_gu, l.mg_down):
+                if m is not None:
+                    n += m.nbytes
+        return n
 
     @property
     def nbytes(self) -> int:
@@ -258,6 +295,16 @@ class LlamaModel:
         self.argmax_slots = torch.zeros(R, ops.ARGMAX_SLOTS, dtype=torch.int64, device=self.dev)
         self._graphs: Dict[tuple, torch.cuda.CUDAGraph] = {}
         self.launches_per_forward = 0
+        # batches of up to 8 rows: "w4a16" (default; bf16 activations on the tensor-core GEMV,
+        # ops/mg.py) or "w4a8" (int8 activation blocks on the dp4a GEMV, opt-in)
+        self.small_batch = os.environ.get("HK_SMALL_BATCH", "w4a16")
+        if self.small_batch not in ("w4a16", "w4a8"):
+            raise ValueError(f"HK_SMALL_BATCH must be w4a16 or w4a8, not {self.small_batch!r}")
+        self.hfrag = None
+        if self.small_batch == "w4a16":
+            weights.prepare_mg()
+            if any(lw.mg_gu is not None for lw in weights.layers):
+                self.hfrag = mg.FragAct(max(lw.w_down.K for lw in weights.layers if lw.mg_gu is not None), self.dev)
 
     def num_splits(self, rows: int) -> int:
         """KV splits per (row, kv head): the smallest power of two (at most 8, the portable
@@ -313,6 +360,8 @@ class LlamaModel:
             if tc:
                 self._attention_block_tc(l, lw, rows, splits)
                 self._ffn_block_tc(lw, rows)
+            elif self._mg_layer(lw):
+                self._layer_mg(l, lw, rows, splits)
             else:
                 self._attention_block_gemv(l, lw, rows, splits)
                 if lw.moe is not None:
@@ -348,6 +397,17 @@ class LlamaModel:
                 src = self.xb.index_select(0, self.logit_rows[:nl].long())
             self.logits[:nl].zero_()
             ops.tc_gemm(w.lm_head, src, self.logits[:nl], self.status, y_zeroed=True)
+        elif self.small_batch == "w4a16" and w.mg_head is not None:
+            src = x
+            if n_logits:
+                src = self.x.index_select(0, self.logit_rows[:nl].long())
+            fuse = sample == "greedy"
+            self._gemv_cols(lambda c0, c1: mg.gemv(w.mg_head, c1 - c0, x_norm=(src[c0:c1], w.out_norm, cfg.eps),
+                                                   y=self.logits[c0:c1], status=self.status,
+                                                   argmax_slots=self.argmax_slots[c0:c1] if fuse else None), nl)
+            if fuse:
+                ops.argmax_finalize(self.argmax_slots, nl, self.next_ids)
+                sample = "done"
         else:
             ops.rmsnorm_q8(x, w.out_norm, cfg.eps, self.xa.view(rows))
             xa = self.xa
@@ -385,6 +445,30 @@ class LlamaModel:
                              inp.row_ctx[:rows], self.scale, splits, self.part_o, self.part_lse,
                              out_q8=out_q8, out_bf16=out_bf16, counters=self.attn_counters)
 
+    # ---- W4A16 small-batch path (ops/mg.py) ----
+    def _mg_layer(self, lw) -> bool:
+        return self.small_batch == "w4a16" and lw.mg_ready()
+
+    def _layer_mg(self, l, lw, rows, splits):
+        """One layer for up to 8 rows per launch: fused RMSNorm -> QKV, RoPE + paged append,
+        split-KV attention (bf16 out), O projection + residual, fused RMSNorm -> gate/up + SwiGLU
+        (h in fragment order), down projection + residual. Five launches per 8 rows."""
+        cfg, x, st = self.cfg, self.x, self.status
+        self._gemv_cols(lambda c0, c1: mg.gemv(lw.mg_qkv, c1 - c0, x_norm=(x[c0:c1], lw.attn_norm, cfg.eps),
+                                               y=self.qkv[c0:c1], status=st), rows)
+        self._rope_attention(l, lw, rows, splits, out_bf16=self.attb[:rows])
+        self._gemv_cols(lambda c0, c1: mg.gemv(lw.mg_o, c1 - c0, xb=self.attb[c0:c1], y=x[c0:c1], residual=True,
+                                               status=st), rows)
+        if lw.moe is not None:
+            ops.rmsnorm_q8(x[:rows], lw.ffn_norm, cfg.eps, self.xa.view(rows))
+            lw.moe.forward(self, rows)
+            return
+
+        def ffn(c0, c1):
+            mg.gemv(lw.mg_gu, c1 - c0, x_norm=(x[c0:c1], lw.ffn_norm, cfg.eps), hfrag=self.hfrag, status=st)
+            mg.gemv(lw.mg_down, c1 - c0, xfrag=self.hfrag, y=x[c0:c1], residual=True, status=st)
+        self._gemv_cols(ffn, rows)
+
     def _attention_block_gemv(self, l, lw, rows, splits):
         x = self.x[:rows]
         ops.rmsnorm_q8(x, lw.attn_norm, self.cfg.eps, self.xa.view(rows))
@@ -403,10 +487,46 @@ class LlamaModel:
                                                 residual=True, prefetch=ffn_next if c0 == 0 else None), rows)
 
     # ---- tensor parallel (decode GEMV path: fused push all-reduce; see parallel/tp.py) ----
+    def _tp_norm_out(self, l_next: int, rows: int):
+        """Output form of an all-reduce site whose normalised rows feed layer ``l_next`` (or the LM
+        head when l_next == layers): bf16 rows for the W4A16 GEMV, q8 blocks for the dp4a GEMV."""
+        w = self.w
+        if l_next < len(w.layers):
+            bf16 = self._mg_layer(w.layers[l_next])
+        else:
+            bf16 = self.small_batch == "w4a16" and w.mg_head is not None
+        return (None, self.xb[:rows]) if bf16 else (self.xa.view(rows), None)
+
+    def _layer_mg_tp(self, l, lw, rows, splits):
+        """Tensor-parallel layer on the W4A16 GEMV: the row-parallel projections push their
+        partials (flagged words over NVLink) and the all-reduce + RMSNorm kernel leaves bf16
+        normalised rows for the next column-parallel projection."""
+        cfg, w, tp, st = self.cfg, self.w, self.tp, self.status
+        xa_res, xb_res = self.x[:rows], self.x2[:rows]
+        if l == 0:
+            mg.gemv(lw.mg_qkv, rows, x_norm=(xa_res, lw.attn_norm, cfg.eps), y=self.qkv[:rows], status=st)
+        else:  # the previous layer's all-reduce left norm(x) (bf16) in self.xb
+            mg.gemv(lw.mg_qkv, rows, xb=self.xb[:rows], y=self.qkv[:rows], status=st)
+        self._rope_attention(l, lw, rows, splits, out_bf16=self.attb[:rows])
+        mg.gemv(lw.mg_o, rows, xb=self.attb[:rows], push=(tp.push_recv[2 * l], tp.epoch), status=st)
+        if lw.moe is not None:
+            ops.tp_allreduce_rmsnorm_q8(tp, 2 * l, xa_res, xb_res, lw.ffn_norm, cfg.eps, self.xa.view(rows))
+            lw.moe.forward_ep(self, rows, 2 * l + 1)
+        else:
+            ops.tp_allreduce_rmsnorm_q8(tp, 2 * l, xa_res, xb_res, lw.ffn_norm, cfg.eps, out_bf16=self.xb[:rows])
+            mg.gemv(lw.mg_gu, rows, xb=self.xb[:rows], hfrag=self.hfrag, status=st)
+            mg.gemv(lw.mg_down, rows, xfrag=self.hfrag, push=(tp.push_recv[2 * l + 1], tp.epoch), status=st)
+        nxt = w.layers[l + 1].attn_norm if l + 1 < len(w.layers) else w.out_norm
+        q8, bf = self._tp_norm_out(l + 1, rows)
+        ops.tp_allreduce_rmsnorm_q8(tp, 2 * l + 1, xb_res, xa_res, nxt, cfg.eps, q8, bf)
+
     def _layer_gemv_tp(self, l, lw, rows, splits):
         cfg, w, tp = self.cfg, self.w, self.tp
         if rows > GEMV_COLS:
             raise RuntimeError("tensor-parallel GEMV path takes at most 8 rows")
+        if self._mg_layer(lw):
+            self._layer_mg_tp(l, lw, rows, splits)
+            return
         xa_res, xb_res = self.x[:rows], self.x2[:rows]
         if l == 0:
             ops.rmsnorm_q8(xa_res, lw.attn_norm, cfg.eps, self.xa.view(rows))
@@ -428,7 +548,8 @@ class LlamaModel:
                             prefetch=[lw.w_down])
             ops.gemv_push(lw.w_down, self._q8_slice(self.hq, 0, rows, lw.w_down.K), tp, 2 * l + 1, prefetch=nxt)
         nxt = w.layers[l + 1].attn_norm if l + 1 < len(w.layers) else w.out_norm
-        ops.tp_allreduce_rmsnorm_q8(tp, 2 * l + 1, xb_res, xa_res, nxt, cfg.eps, self.xa.view(rows))
+        q8, bf = self._tp_norm_out(l + 1, rows)
+        ops.tp_allreduce_rmsnorm_q8(tp, 2 * l + 1, xb_res, xa_res, nxt, cfg.eps, q8, bf)
 
     def _allreduce_partial_tc(self, rows):
         """Prefill (tensor-core path): NCCL all-reduce of this rank's partial, added to x."""
@@ -443,6 +564,22 @@ class LlamaModel:
         if sample not in ("greedy", "none"):
             raise NotImplementedError("tensor-parallel sampling: greedy only")
         if n_logits < 0:
+            return
+        if self.small_batch == "w4a16" and w.mg_head is not None:
+            off = tp.rank * w.lm_head.N
+            if tc or n_logits:
+                src = self.x[:rows]
+                if n_logits:
+                    src = self.x.index_select(0, self.logit_rows[:nl].long())
+                kw = lambda c0, c1: dict(x_norm=(src[c0:c1], w.out_norm, cfg.eps))  # noqa: E731
+            else:  # the last layer's all-reduce left norm(x) (bf16) in self.xb
+                kw = lambda c0, c1: dict(xb=self.xb[c0:c1])  # noqa: E731
+            greedy = sample != "none"
+            self._gemv_cols(lambda c0, c1: mg.gemv(w.mg_head, c1 - c0, y=self.logits[c0:c1], status=self.status,
+                                                   argmax_slots=self.argmax_slots[c0:c1] if greedy else None,
+                                                   argmax_offset=off, **kw(c0, c1)), nl)
+            if greedy:
+                ops.tp_argmax(tp, self.argmax_slots, nl, self.next_ids)
             return
         if tc or n_logits:
             # the residual is in self.x; normalise the sampled rows here

@@ -109,11 +109,15 @@ def tp_begin(tp):
     kernels().tp_begin(tp.epoch, PDL)
 
 
-def tp_allreduce_rmsnorm_q8(tp, site: int, x_in: torch.Tensor, x_out: torch.Tensor, w, eps: float, out: Q8Act):
-    """x_out = x_in + sum of every rank's partials at ``site``; then RMSNorm -> q8 (``out``)."""
+def tp_allreduce_rmsnorm_q8(tp, site: int, x_in: torch.Tensor, x_out: torch.Tensor, w, eps: float,
+                            out: Optional[Q8Act] = None, out_bf16: Optional[torch.Tensor] = None):
+    """x_out = x_in + sum of every rank's partials at ``site``; then RMSNorm -> q8 (``out``) or
+    bf16 rows (``out_bf16``)."""
     launches.add()
     kernels().tp_allreduce_rmsnorm_q8(x_in, x_out, tp.recv_local(site), tp.rank_stride, tp.world, tp.epoch, w, eps,
-                                       out.q, out.d, out.s, tp.status, PDL)
+                                       out.q if out is not None else None, out.d if out is not None else None,
+                                       out.s if out is not None else None, tp.status, PDL, yb=out_bf16,
+                                       wait_ns=getattr(tp, "wait_ns", 0))
 
 
 def tp_argmax(tp, slots: torch.Tensor, rows: int, out: torch.Tensor):
@@ -122,7 +126,7 @@ def tp_argmax(tp, slots: torch.Tensor, rows: int, out: torch.Tensor):
     if rows > tp.key_rows:
         raise ValueError(f"tp_argmax: {rows} rows exceed the key region ({tp.key_rows})")
     kernels().tp_argmax(slots, rows, tp.key_rows, tp.keys_table, tp.base + tp.keys_off, tp.argmax_uses, tp.rank, out,
-                        tp.status, PDL)
+                        tp.status, PDL, wait_ns=getattr(tp, "wait_ns", 0))
 
 
 def argmax_finalize(slots: torch.Tensor, rows: int, out: torch.Tensor):

@@ -20,6 +20,8 @@ from __future__ import annotations
 
 from typing import List, Optional
 
+import os
+
 import torch
 import torch.distributed as dist
 
@@ -162,6 +164,8 @@ class TPComm:
         self.epoch = torch.zeros(1, dtype=torch.int32, device=self.dev)       # forwards on the push path
         self.argmax_uses = torch.zeros(1, dtype=torch.int32, device=self.dev)  # greedy rounds
         self.status = torch.zeros(1, dtype=torch.int32, device=self.dev)
+        # bound of every peer wait in the fused collectives, in ns (0: the kernels' default, 1 s)
+        self.wait_ns = int(os.environ.get("HK_TP_WAIT_NS", "0"))
 
         def table(vals):
             return torch.tensor(vals, dtype=torch.int64, device=self.dev)

@@ -115,10 +115,9 @@ class ServeLoop:
         if not self.engine.has_work():
             return 0
         try:
+            # the engine reads every device status word after each step and raises before
+            # committing tokens when one is set (e.g. a peer's collective timed out)
             events = self.engine.step()
-            tp = getattr(getattr(self.engine, "model", None), "tp", None)
-            if tp is not None and self.steps % 16 == 0:
-                tp.check()  # a peer's collective timed out (device status word)
         except Exception as e:  # noqa: BLE001 - the step failed: drain and report
             self._engine_failed(e)
             return 0
