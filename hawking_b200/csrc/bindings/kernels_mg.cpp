@@ -56,8 +56,8 @@ void mg_gemv(int64_t fmt, int64_t xin, int64_t epi, const Tensor& tiles, int64_t
   TORCH_CHECK(tiles.numel() == G * KT * hk::mg_tile_bytes((int)fmt) && KT * 256 == K, "mg_gemv: tile shape mismatch");
   TORCH_CHECK(nb >= 1 && nb <= 8, "mg_gemv: batch columns must be 1..8");
   const int dev = tiles.device().index();
-  const int grid = num_sms(dev);
-  TORCH_CHECK(part.is_cuda() && part.scalar_type() == at::kFloat && part.numel() >= (int64_t)grid * 8 * 2 * 32 * 4,
+  const int sms = num_sms(dev);
+  TORCH_CHECK(part.is_cuda() && part.scalar_type() == at::kFloat && part.numel() >= (int64_t)sms * 2 * 8 * 2 * 32 * 4,
               "mg_gemv: partial scratch too small");
   TORCH_CHECK(counters.is_cuda() && counters.scalar_type() == at::kInt && counters.numel() >= G,
               "mg_gemv: counters too small");
@@ -130,7 +130,7 @@ void mg_gemv(int64_t fmt, int64_t xin, int64_t epi, const Tensor& tiles, int64_t
   a.counters = counters.data_ptr<int>();
   a.status = status.data_ptr<int>();
   const c10::cuda::CUDAGuard g(tiles.device());
-  hk::mg_gemv_launch((int)fmt, (int)xin, (int)epi, a, grid, cur_stream(), pdl);
+  hk::mg_gemv_launch((int)fmt, (int)xin, (int)epi, a, sms, cur_stream(), pdl);
 }
 }  // namespace
 

@@ -141,7 +141,7 @@ struct MgArgs {
   unsigned long long* const* push_recv;  // PUSH: as GemvArgs
   const int* push_epoch;
   int push_n;
-  // scratch: partial fragments [gridDim.x * 8 warps][2][32] float4, zeroed counters [G]
+  // scratch: partial fragments [SMs * 2 CTAs * 8 warps][2][32] float4, zeroed counters [G]
   float4* part;
   int* counters;
   int* status;
@@ -150,7 +150,7 @@ int mg_tile_bytes(int fmt);
 size_t mg_smem_bytes(int fmt, int xin, int nb, int K);
 // rowmap[G * 16]: source row of each tile row (-1: zero row)
 void mg_pack_launch(int fmt, const WPlanes& w, const int* rowmap, int G, int KT, uint8_t* out, cudaStream_t s);
-void mg_gemv_launch(int fmt, int xin, int epi, const MgArgs& a, int grid, cudaStream_t s, bool pdl);
+void mg_gemv_launch(int fmt, int xin, int epi, const MgArgs& a, int sms, cudaStream_t s, bool pdl);
 
 // ---- decode ops (decode_ops.cu, attention.cu) ----
 

@@ -7,7 +7,8 @@
 //    in the register-fragment order of mma.sync m16n8k16 (lane t of a warp finds the 8 nibbles of
 //    its A fragment for one k-step in one 32-bit word, four k-steps per 16-byte load). Tiles are
 //    stored row-group major, so any contiguous range of tiles is one contiguous byte range.
-//  * Streaming. The tiles are split into gridDim.x * 8 contiguous, equal ranges, one per warp. Each
+//  * Streaming. The tiles are split into gridDim.x * 8 contiguous, equal ranges, one per warp (two
+//    CTAs of 8 warps per SM). Each
 //    warp owns a 4-deep ring of tile buffers in shared memory filled by cp.async.bulk (the TMA copy
 //    engine, completing on an mbarrier); lane 0 issues the first four copies before the
 //    programmatic-dependent-launch wait, so a kernel's weights stream in while the kernel before it
@@ -51,6 +52,7 @@ constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 constexpr int kStages = 4;
 constexpr int kScaleBytes = 16 * 8 * 8;  // per warp: [16 rows][8 sub-blocks] float2 (S16, M'')
+constexpr int kMaxCtasPerSm = 2;         // resident CTAs per SM (the partial scratch is sized for this)
 
 template <int FMT> struct Tile;
 template <> struct Tile<WF_Q4_K> {
@@ -251,8 +253,18 @@ __device__ __forceinline__ void stage_x(const MgArgs& a, uint4* xs, int64_t cstr
   __syncthreads();
 }
 
-// Last piece (warp range) holding tile t: pieces p own [p*T/P, (p+1)*T/P).
+// Last piece (warp range) holding tile t: pieces p own [p*T/P, (p+1)*T/P). When T < P some
+// pieces are empty; owner() always names the non-empty one.
 __device__ __forceinline__ int64_t owner(int64_t t, int64_t T, int64_t P) { return ((t + 1) * P - 1) / T; }
+// The non-empty piece after `p` whose range continues past p's end.
+__device__ __forceinline__ int64_t next_owner(int64_t p, int64_t T, int64_t P) { return owner((p + 1) * T / P, T, P); }
+// Number of distinct pieces holding tiles of row group g (tiles [g*KT, (g+1)*KT)).
+__device__ __forceinline__ int pieces_of_group(int64_t g, int KT, int64_t T, int64_t P) {
+  const int64_t last = g * KT + KT - 1;
+  int n = 1;
+  for (int64_t pp = owner(g * KT, T, P); (pp + 1) * T / P <= last; pp = next_owner(pp, T, P)) ++n;
+  return n;
+}
 
 template <int FMT, int NB, int XIN, int EPI>
 __global__ void __launch_bounds__(kThreads, 2) mg_gemv_kernel(MgArgs a) {
@@ -332,16 +344,18 @@ __global__ void __launch_bounds__(kThreads, 2) mg_gemv_kernel(MgArgs a) {
       int old = 0;
       if (lane == 0) old = atomicAdd(a.counters + g, 1);
       old = __shfl_sync(0xffffffffu, old, 0);
-      if (old == (int)(pl - pf)) {
+      if (old == pieces_of_group(g, a.KT, T, P) - 1) {
         __threadfence();
         float v[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int64_t pp = pf; pp <= pl; ++pp) {
+        // the contributing pieces in piece order (a fixed summation order); empty pieces skipped
+        for (int64_t pp = pf;; pp = next_owner(pp, T, P)) {
           const int sl = ((pp * T / P) / a.KT == g) ? 0 : 1;
           const float4 pv = __ldcg(a.part + (pp * 2 + sl) * 32 + lane);
           v[0] += pv.x;
           v[1] += pv.y;
           v[2] += pv.z;
           v[3] += pv.w;
+          if (pp == pl) break;
         }
         if (lane == 0) a.counters[g] = 0;
         epilogue<EPI>(a, g, v, lane);
@@ -363,11 +377,14 @@ size_t smem_bytes(int fmt, int xin, int nb, int K) {
 }
 
 template <int FMT, int XIN, int EPI>
-void dispatch_nb(const MgArgs& a, int grid, cudaStream_t st, bool pdl) {
+void dispatch_nb(const MgArgs& a, int sms, cudaStream_t st, bool pdl) {
   const size_t smem = smem_bytes(FMT, XIN, a.nb, a.K);
   auto go = [&](auto kern) {
     HK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    launch(kern, dim3(grid), dim3(kThreads), smem, st, pdl, a);
+    int per_sm = 1;
+    HK_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem));
+    per_sm = per_sm < 1 ? 1 : (per_sm > kMaxCtasPerSm ? kMaxCtasPerSm : per_sm);
+    launch(kern, dim3(sms * per_sm), dim3(kThreads), smem, st, pdl, a);
   };
   if (a.nb == 1) go(mg_gemv_kernel<FMT, 1, XIN, EPI>);
   else if (a.nb == 2) go(mg_gemv_kernel<FMT, 2, XIN, EPI>);
@@ -437,7 +454,7 @@ void mg_pack_launch(int fmt, const WPlanes& w, const int* rowmap, int G, int KT,
   HK_CUDA_CHECK(cudaGetLastError());
 }
 
-void mg_gemv_launch(int fmt, int xin, int epi, const MgArgs& a, int grid, cudaStream_t s, bool pdl) {
+void mg_gemv_launch(int fmt, int xin, int epi, const MgArgs& a, int sms, cudaStream_t s, bool pdl) {
   if (fmt != WF_Q4_K) throw std::runtime_error("mg_gemv: format not supported");
   if (a.nb < 1 || a.nb > 8) throw std::runtime_error("mg_gemv: batch columns must be 1..8");
   if (a.K % 256) throw std::runtime_error("mg_gemv: K must be a multiple of 256");
@@ -450,9 +467,9 @@ void mg_gemv_launch(int fmt, int xin, int epi, const MgArgs& a, int grid, cudaSt
     throw std::runtime_error("mg_gemv push: peer tables required");
   if (!a.part || !a.counters) throw std::runtime_error("mg_gemv: scratch required");
   switch (xin) {
-    case MG_X_NORM: mg::dispatch_epi<WF_Q4_K, MG_X_NORM>(epi, a, grid, s, pdl); break;
-    case MG_X_BF16: mg::dispatch_epi<WF_Q4_K, MG_X_BF16>(epi, a, grid, s, pdl); break;
-    case MG_X_FRAG: mg::dispatch_epi<WF_Q4_K, MG_X_FRAG>(epi, a, grid, s, pdl); break;
+    case MG_X_NORM: mg::dispatch_epi<WF_Q4_K, MG_X_NORM>(epi, a, sms, s, pdl); break;
+    case MG_X_BF16: mg::dispatch_epi<WF_Q4_K, MG_X_BF16>(epi, a, sms, s, pdl); break;
+    case MG_X_FRAG: mg::dispatch_epi<WF_Q4_K, MG_X_FRAG>(epi, a, sms, s, pdl); break;
     default: throw std::runtime_error("mg_gemv: bad input mode");
   }
 }
