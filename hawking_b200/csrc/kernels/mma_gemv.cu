@@ -123,27 +123,26 @@ struct XFrag {
 template <int NB>
 __device__ __forceinline__ void consume_q4k(const uint8_t* tile, int s, const XFrag& x, float2* scs, int lane,
                                             float (&sum)[4]) {
-  decode_scales_q4k(tile, scs, lane);
   const int n = lane >> 2, q = lane & 3, r0 = lane >> 2;
+  // every load of the tile first (quants, activation fragments), so they are in flight together
   const uint4* qp = reinterpret_cast<const uint4*>(tile + 256) + lane;
   uint4 qv[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) qv[j] = qp[j * 32];
-  __syncwarp();  // scales visible to every lane
   const bool has_col = n < NB;
   const uint4* xp = x.p + (int64_t)n * x.cstride + ((int64_t)(4 * s) * 4 + q) * 2;
+  uint4 xv[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) xv[j] = has_col ? xp[(j >> 1) * 8 + (j & 1)] : make_uint4(0, 0, 0, 0);
+  decode_scales_q4k(tile, scs, lane);
+  __syncwarp();  // scales visible to every lane
   constexpr uint32_t ONES = 0x3F803F80u;
   constexpr uint32_t M = 0x00780078u;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {  // k-step groups of 4 (two sub-blocks)
-    uint4 b01 = make_uint4(0, 0, 0, 0), b23 = make_uint4(0, 0, 0, 0);
-    if (has_col) {
-      b01 = xp[j * 8];
-      b23 = xp[j * 8 + 1];
-    }
 #pragma unroll
     for (int h = 0; h < 2; ++h) {  // sub-block 2j + h = k-steps 4j + 2h, 4j + 2h + 1
-      const uint4 b = h ? b23 : b01;
+      const uint4 b = xv[2 * j + h];
       float c[4] = {0.f, 0.f, 0.f, 0.f}, e[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int kk = 0; kk < 2; ++kk) {
