@@ -121,15 +121,15 @@ struct XFrag {
 // One tile: 16 rows x 256 columns (super-block s) accumulated into sum[4] (the lane's C fragment:
 // rows r0, r0 + 8 x columns 2q, 2q + 1).
 template <int NB>
-__device__ __forceinline__ void consume_q4k(const uint8_t* tile, int s, const XFrag& x, float2* scs, int lane,
-                                            float (&sum)[4]) {
+__device__ __forceinline__ void consume_q4k(const uint8_t* tile, int s, const XFrag& x, int nb, float2* scs,
+                                            int lane, float (&sum)[4]) {
   const int n = lane >> 2, q = lane & 3, r0 = lane >> 2;
   // every load of the tile first (quants, activation fragments), so they are in flight together
   const uint4* qp = reinterpret_cast<const uint4*>(tile + 256) + lane;
   uint4 qv[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) qv[j] = qp[j * 32];
-  const bool has_col = n < NB;
+  const bool has_col = n < nb;  // columns nb..NB-1 of the fragment are not staged: they read as 0
   const uint4* xp = x.p + (int64_t)n * x.cstride + ((int64_t)(4 * s) * 4 + q) * 2;
   uint4 xv[8];
 #pragma unroll
@@ -322,7 +322,7 @@ __global__ void __launch_bounds__(kThreads, 2) mg_gemv_kernel(MgArgs a) {
     const int64_t ti = t0 + i;
     const int64_t g = ti / a.KT;
     const int s = (int)(ti - g * a.KT);
-    consume_q4k<NB>(ring + st * TB, s, x, scs, lane, sum);  // ends with __syncwarp: the stage is free
+    consume_q4k<NB>(ring + st * TB, s, x, a.nb, scs, lane, sum);  // ends with __syncwarp: the stage is free
     if (i + kStages < n_tiles) {
       if (lane == 0) {
         sm100::fence_proxy_async_smem();  // this stage's generic reads before the async overwrite
