@@ -120,7 +120,7 @@ struct XFrag {
 
 // One tile: 16 rows x 256 columns (super-block s) accumulated into sum[4] (the lane's C fragment:
 // rows r0, r0 + 8 x columns 2q, 2q + 1).
-template <int NB>
+template <int NB, bool XGLOBAL>
 __device__ __forceinline__ void consume_q4k(const uint8_t* tile, int s, const XFrag& x, int nb, float2* scs,
                                             int lane, float (&sum)[4]) {
   const int n = lane >> 2, q = lane & 3, r0 = lane >> 2;
@@ -130,10 +130,13 @@ __device__ __forceinline__ void consume_q4k(const uint8_t* tile, int s, const XF
 #pragma unroll
   for (int j = 0; j < 4; ++j) qv[j] = qp[j * 32];
   const bool has_col = n < nb;  // columns nb..NB-1 of the fragment are not staged: they read as 0
-  const uint4* xp = x.p + (int64_t)n * x.cstride + ((int64_t)(4 * s) * 4 + q) * 2;
+  const uint4* xp = x.p + (n * (int)x.cstride + s * 32 + q * 2);
   uint4 xv[8];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) xv[j] = has_col ? xp[(j >> 1) * 8 + (j & 1)] : make_uint4(0, 0, 0, 0);
+  for (int j = 0; j < 8; ++j) {
+    if (XGLOBAL) xv[j] = has_col ? __ldg(xp + (j >> 1) * 8 + (j & 1)) : make_uint4(0, 0, 0, 0);
+    else xv[j] = has_col ? xp[(j >> 1) * 8 + (j & 1)] : make_uint4(0, 0, 0, 0);
+  }
   decode_scales_q4k(tile, scs, lane);
   __syncwarp();  // scales visible to every lane
   constexpr uint32_t ONES = 0x3F803F80u;
@@ -171,7 +174,8 @@ __device__ __forceinline__ void frag_store_bf16(__nv_bfloat16* base, int64_t cst
 }
 
 template <int EPI>
-__device__ __forceinline__ void epilogue(const MgArgs& a, int64_t g, const float (&v)[4], int lane) {
+__device__ __forceinline__ void epilogue(const MgArgs& a, uint32_t g_, const float (&v)[4], int lane) {
+  const int64_t g = g_;
   const int r0 = lane >> 2, q = lane & 3;
   if constexpr (EPI == MG_SWIGLU) {
     const int64_t o = g * 8 + r0;  // output row: gate in tile row r0, up in r0 + 8
@@ -254,14 +258,18 @@ __device__ __forceinline__ void stage_x(const MgArgs& a, uint4* xs, int64_t cstr
 
 // Last piece (warp range) holding tile t: pieces p own [p*T/P, (p+1)*T/P). When T < P some
 // pieces are empty; owner() always names the non-empty one.
-__device__ __forceinline__ int64_t owner(int64_t t, int64_t T, int64_t P) { return ((t + 1) * P - 1) / T; }
+// 32-bit arithmetic: the launcher checks T * P < 2^32.
+__device__ __forceinline__ uint32_t owner(uint32_t t, uint32_t T, uint32_t P) { return ((t + 1) * P - 1) / T; }
+__device__ __forceinline__ uint32_t start_of(uint32_t p, uint32_t T, uint32_t P) { return p * T / P; }
 // The non-empty piece after `p` whose range continues past p's end.
-__device__ __forceinline__ int64_t next_owner(int64_t p, int64_t T, int64_t P) { return owner((p + 1) * T / P, T, P); }
+__device__ __forceinline__ uint32_t next_owner(uint32_t p, uint32_t T, uint32_t P) {
+  return owner(start_of(p + 1, T, P), T, P);
+}
 // Number of distinct pieces holding tiles of row group g (tiles [g*KT, (g+1)*KT)).
-__device__ __forceinline__ int pieces_of_group(int64_t g, int KT, int64_t T, int64_t P) {
-  const int64_t last = g * KT + KT - 1;
+__device__ __forceinline__ int pieces_of_group(uint32_t g, uint32_t KT, uint32_t T, uint32_t P) {
+  const uint32_t last = g * KT + KT - 1;
   int n = 1;
-  for (int64_t pp = owner(g * KT, T, P); (pp + 1) * T / P <= last; pp = next_owner(pp, T, P)) ++n;
+  for (uint32_t pp = owner(g * KT, T, P); start_of(pp + 1, T, P) <= last; pp = next_owner(pp, T, P)) ++n;
   return n;
 }
 
@@ -276,11 +284,12 @@ __global__ void __launch_bounds__(kThreads, 2) mg_gemv_kernel(MgArgs a) {
   float* red = reinterpret_cast<float*>(smem + kWarps * (kStages * TB + kScaleBytes) + kWarps * kStages * 8);
   uint4* xs = reinterpret_cast<uint4*>(smem + kWarps * (kStages * TB + kScaleBytes) + kWarps * kStages * 8 + 128);
 
-  const int64_t T = (int64_t)a.G * a.KT;
-  const int64_t P = (int64_t)gridDim.x * kWarps;
-  const int64_t p = (int64_t)blockIdx.x * kWarps + warp;
-  const int64_t t0 = p * T / P, t1 = (p + 1) * T / P;
+  const uint32_t T = (uint32_t)a.G * (uint32_t)a.KT;
+  const uint32_t P = gridDim.x * kWarps;
+  const uint32_t p = blockIdx.x * kWarps + warp;
+  const uint32_t t0 = start_of(p, T, P), t1 = start_of(p + 1, T, P);
   const int n_tiles = (int)(t1 - t0);
+  const uint32_t KT = (uint32_t)a.KT;
 
   if (lane == 0) {
     for (int s = 0; s < kStages; ++s) sm100::mbar_init(&bars[s], 1);
@@ -290,7 +299,7 @@ __global__ void __launch_bounds__(kThreads, 2) mg_gemv_kernel(MgArgs a) {
   auto issue = [&](int i) {
     const int st = i % kStages;
     sm100::mbar_arrive_expect_tx(&bars[st], TB);
-    sm100::bulk_g2s(ring + st * TB, a.tiles + (t0 + i) * (int64_t)TB, TB, &bars[st]);
+    sm100::bulk_g2s(ring + st * TB, a.tiles + (int64_t)(t0 + i) * TB, TB, &bars[st]);
   };
   // weights first: they do not depend on the previous kernel
   int issued = n_tiles < kStages ? n_tiles : kStages;  // same value on every lane
@@ -313,16 +322,15 @@ __global__ void __launch_bounds__(kThreads, 2) mg_gemv_kernel(MgArgs a) {
   float sum[4] = {0.f, 0.f, 0.f, 0.f};
   int i = 0;
   bool ok = true;
+  uint32_t g = t0 / KT, s = t0 - g * KT;  // row group and column tile, advanced incrementally
+  const uint32_t first_g = g;
   for (; i < n_tiles; ++i) {
     const int st = i % kStages;
     if (!sm100::mbar_wait(&bars[st], (uint32_t)((i / kStages) & 1), a.status)) {
       ok = false;
       break;
     }
-    const int64_t ti = t0 + i;
-    const int64_t g = ti / a.KT;
-    const int s = (int)(ti - g * a.KT);
-    consume_q4k<NB>(ring + st * TB, s, x, a.nb, scs, lane, sum);  // ends with __syncwarp: the stage is free
+    consume_q4k<NB, XIN == MG_X_FRAG>(ring + st * TB, (int)s, x, a.nb, scs, lane, sum);  // ends with __syncwarp
     if (i + kStages < n_tiles) {
       if (lane == 0) {
         sm100::fence_proxy_async_smem();  // this stage's generic reads before the async overwrite
@@ -330,26 +338,27 @@ __global__ void __launch_bounds__(kThreads, 2) mg_gemv_kernel(MgArgs a) {
       }
       issued = i + kStages + 1;
     }
-    const bool last = (i == n_tiles - 1) || ((ti + 1) / a.KT != g);
+    const bool last = (i == n_tiles - 1) || (s == KT - 1);
+    if (++s == KT) s = 0;
     if (!last) continue;
     // row group g done for this warp: direct epilogue, or partial + deterministic fix-up
-    const int64_t pf = owner(g * a.KT, T, P), pl = owner(g * a.KT + a.KT - 1, T, P);
+    const uint32_t pf = owner(g * KT, T, P), pl = owner(g * KT + KT - 1, T, P);
     if (pf == pl) {
       epilogue<EPI>(a, g, sum, lane);
     } else {
-      const int slot = (t0 / a.KT == g) ? 0 : 1;
-      __stcg(a.part + (p * 2 + slot) * 32 + lane, make_float4(sum[0], sum[1], sum[2], sum[3]));
+      const int slot = (g == first_g) ? 0 : 1;
+      __stcg(a.part + ((int64_t)p * 2 + slot) * 32 + lane, make_float4(sum[0], sum[1], sum[2], sum[3]));
       __threadfence();
       int old = 0;
       if (lane == 0) old = atomicAdd(a.counters + g, 1);
       old = __shfl_sync(0xffffffffu, old, 0);
-      if (old == pieces_of_group(g, a.KT, T, P) - 1) {
+      if (old == pieces_of_group(g, KT, T, P) - 1) {
         __threadfence();
         float v[4] = {0.f, 0.f, 0.f, 0.f};
         // the contributing pieces in piece order (a fixed summation order); empty pieces skipped
-        for (int64_t pp = pf;; pp = next_owner(pp, T, P)) {
-          const int sl = ((pp * T / P) / a.KT == g) ? 0 : 1;
-          const float4 pv = __ldcg(a.part + (pp * 2 + sl) * 32 + lane);
+        for (uint32_t pp = pf;; pp = next_owner(pp, T, P)) {
+          const int sl = (start_of(pp, T, P) / KT == g) ? 0 : 1;
+          const float4 pv = __ldcg(a.part + ((int64_t)pp * 2 + sl) * 32 + lane);
           v[0] += pv.x;
           v[1] += pv.y;
           v[2] += pv.z;
@@ -361,6 +370,7 @@ __global__ void __launch_bounds__(kThreads, 2) mg_gemv_kernel(MgArgs a) {
       }
     }
     sum[0] = sum[1] = sum[2] = sum[3] = 0.f;
+    ++g;
   }
   if (!ok && lane == 0) {
     // wait (bounded) for this warp's copies still in flight before the CTA may exit
@@ -465,6 +475,9 @@ void mg_gemv_launch(int fmt, int xin, int epi, const MgArgs& a, int sms, cudaStr
   if (epi == MG_PUSH && (!a.push_recv || !a.push_epoch || a.push_n <= 0))
     throw std::runtime_error("mg_gemv push: peer tables required");
   if (!a.part || !a.counters) throw std::runtime_error("mg_gemv: scratch required");
+  if ((uint64_t)a.G * a.KT * ((uint64_t)sms * mg::kMaxCtasPerSm * mg::kWarps + 1) >= (1ull << 32))
+    throw std::runtime_error("mg_gemv: matrix too large for 32-bit tile arithmetic");
+  if ((int64_t)a.nb * (a.K / 64 * 8 + 1) >= (1ll << 31)) throw std::runtime_error("mg_gemv: activation index overflow");
   switch (xin) {
     case MG_X_NORM: mg::dispatch_epi<WF_Q4_K, MG_X_NORM>(epi, a, sms, s, pdl); break;
     case MG_X_BF16: mg::dispatch_epi<WF_Q4_K, MG_X_BF16>(epi, a, sms, s, pdl); break;

@@ -44,7 +44,12 @@ def test_mg_store_bf16_input(N, K, nb):
     mw = mg.pack(w)
     xb = _x(nb, K, nb).bfloat16()
     y = torch.full((nb, N), float("nan"), device=DEV)
-    mg.gemv(mw, nb, xb=xb, y=y)
+    if nb * K * 2 > 96 * 1024:  # too wide to stage in shared memory: fragment-order input
+        xf = mg.FragAct(K, DEV)
+        xf.buf.view(-1)[mg.frag_index(K, nb, xf.cstride, DEV)] = xb.reshape(-1)
+        mg.gemv(mw, nb, xfrag=xf, y=y)
+    else:
+        mg.gemv(mw, nb, xb=xb, y=y)
     _status_ok()
     _close(y, _ref(w, xb))
 
