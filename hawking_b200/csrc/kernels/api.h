@@ -111,7 +111,7 @@ void gemv_launch(int fmt, int epi, const GemvArgs& a, int nb, cudaStream_t s, bo
 // ---- full-precision small-batch GEMV on the tensor cores (mma_gemv.cu) ----
 // W4A16: weights in fragment-ordered tiles of 16 rows x 256 columns (mg_pack_launch), bf16
 // activations, fp32 accumulation. See mma_gemv.cu for the design.
-enum MgInput : int { MG_X_NORM = 0, MG_X_BF16 = 1, MG_X_FRAG = 2 };
+enum MgInput : int { MG_X_NORM = 0, MG_X_BF16 = 1, MG_X_FRAG = 2, MG_X_FRAG_SMEM = 3 };  // 3: internal (FRAG staged)
 enum MgEpilogue : int { MG_STORE = 0, MG_RESID = 1, MG_SWIGLU = 2, MG_PUSH = 3 };
 struct MgArgs {
   const uint8_t* tiles;     // [G row groups][KT column tiles][tile bytes]

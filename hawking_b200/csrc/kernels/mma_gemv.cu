@@ -73,6 +73,15 @@ __device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// D = A * B (zero accumulator input): no zeroed registers to materialise per sub-block.
+__device__ __forceinline__ void mma_bf16_z(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                           uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%10,%10,%10};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.f));
+}
+
 __device__ __forceinline__ uint32_t pick(const uint4& v, int i) {
   return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
 }
@@ -146,14 +155,18 @@ __device__ __forceinline__ void consume_q4k(const uint8_t* tile, int s, const XF
 #pragma unroll
     for (int h = 0; h < 2; ++h) {  // sub-block 2j + h = k-steps 4j + 2h, 4j + 2h + 1
       const uint4 b = xv[2 * j + h];
-      float c[4] = {0.f, 0.f, 0.f, 0.f}, e[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int kk = 0; kk < 2; ++kk) {
-        const uint32_t w = pick(qv[j], 2 * h + kk);
-        const uint32_t bx = kk ? b.z : b.x, by = kk ? b.w : b.y;
+      float c[4], e[4];
+      {
+        const uint32_t w = pick(qv[j], 2 * h);
+        mma_bf16_z(c, and_or(w << 3, M, ONES), and_or(w >> 1, M, ONES), and_or(w >> 5, M, ONES),
+                   and_or(w >> 9, M, ONES), b.x, b.y);
+        mma_bf16_z(e, ONES, ONES, ONES, ONES, b.x, b.y);
+      }
+      {
+        const uint32_t w = pick(qv[j], 2 * h + 1);
         mma_bf16(c, and_or(w << 3, M, ONES), and_or(w >> 1, M, ONES), and_or(w >> 5, M, ONES),
-                 and_or(w >> 9, M, ONES), bx, by);
-        mma_bf16(e, ONES, ONES, ONES, ONES, bx, by);
+                 and_or(w >> 9, M, ONES), b.z, b.w);
+        mma_bf16(e, ONES, ONES, ONES, ONES, b.z, b.w);
       }
       const int sb = 2 * j + h;
       const float2 s0 = scs[r0 * 8 + sb], s1 = scs[(r0 + 8) * 8 + sb];
@@ -309,7 +322,24 @@ __global__ void __launch_bounds__(kThreads, 2) mg_gemv_kernel(MgArgs a) {
   pdl_wait();
 
   XFrag x;
-  if constexpr (XIN == MG_X_FRAG) {
+  bool x_ok = true;
+  if constexpr (XIN == MG_X_FRAG_SMEM) {
+    // fragment-order activations copied into shared memory, one bulk copy per column (2K bytes)
+    const int64_t cs = (int64_t)a.K / 64 * 8 + 1;
+    uint64_t* xbar = reinterpret_cast<uint64_t*>(red);  // the reduction scratch is unused in this mode
+    if (threadIdx.x == 0) {
+      sm100::mbar_init(xbar, 1);
+      sm100::fence_barrier_init();
+      const uint32_t colb = (uint32_t)a.K * 2;
+      sm100::mbar_arrive_expect_tx(xbar, colb * (uint32_t)a.nb);
+      for (int n = 0; n < a.nb; ++n)
+        sm100::bulk_g2s(xs + n * cs, a.xfrag + (int64_t)n * a.xfrag_cstride, colb, xbar);
+    }
+    __syncthreads();
+    x_ok = sm100::mbar_wait(xbar, 0, a.status);
+    x.p = xs;
+    x.cstride = cs;
+  } else if constexpr (XIN == MG_X_FRAG) {
     x.p = a.xfrag;
     x.cstride = a.xfrag_cstride;
   } else {
@@ -321,10 +351,10 @@ __global__ void __launch_bounds__(kThreads, 2) mg_gemv_kernel(MgArgs a) {
 
   float sum[4] = {0.f, 0.f, 0.f, 0.f};
   int i = 0;
-  bool ok = true;
+  bool ok = x_ok;  // a failed activation copy skips the tiles (the ring is drained below)
   uint32_t g = t0 / KT, s = t0 - g * KT;  // row group and column tile, advanced incrementally
   const uint32_t first_g = g;
-  for (; i < n_tiles; ++i) {
+  for (; ok && i < n_tiles; ++i) {
     const int st = i % kStages;
     if (!sm100::mbar_wait(&bars[st], (uint32_t)((i / kStages) & 1), a.status)) {
       ok = false;
@@ -382,6 +412,7 @@ size_t smem_bytes(int fmt, int xin, int nb, int K) {
   const size_t tb = (size_t)mg_tile_bytes(fmt);
   size_t s = kWarps * (kStages * tb + kScaleBytes) + kWarps * kStages * 8 + 128;
   if (xin != MG_X_FRAG) s += (size_t)nb * ((size_t)K / 64 * 8 + 1) * 16;
+  (void)0;
   return s;
 }
 
@@ -444,6 +475,9 @@ __global__ void pack_q4k_kernel(const uint8_t* qs, int64_t rb0, const uint8_t* h
 
 }  // namespace mg
 
+// Largest fragment-order activation block copied into shared memory (two CTAs per SM still fit).
+constexpr int64_t kFragSmemMax = 30 * 1024;
+
 int mg_tile_bytes(int fmt) {
   switch (fmt) {
     case WF_Q4_K: return mg::Tile<WF_Q4_K>::BYTES;
@@ -481,7 +515,13 @@ void mg_gemv_launch(int fmt, int xin, int epi, const MgArgs& a, int sms, cudaStr
   switch (xin) {
     case MG_X_NORM: mg::dispatch_epi<WF_Q4_K, MG_X_NORM>(epi, a, sms, s, pdl); break;
     case MG_X_BF16: mg::dispatch_epi<WF_Q4_K, MG_X_BF16>(epi, a, sms, s, pdl); break;
-    case MG_X_FRAG: mg::dispatch_epi<WF_Q4_K, MG_X_FRAG>(epi, a, sms, s, pdl); break;
+    case MG_X_FRAG:
+      // stage the fragment-order activations in shared memory when they fit beside the rings
+      if ((int64_t)a.nb * (a.K / 64 * 8 + 1) * 16 <= kFragSmemMax)
+        mg::dispatch_epi<WF_Q4_K, MG_X_FRAG_SMEM>(epi, a, sms, s, pdl);
+      else
+        mg::dispatch_epi<WF_Q4_K, MG_X_FRAG>(epi, a, sms, s, pdl);
+      break;
     default: throw std::runtime_error("mg_gemv: bad input mode");
   }
 }
