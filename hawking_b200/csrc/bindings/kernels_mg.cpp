@@ -57,7 +57,7 @@ void mg_gemv(int64_t fmt, int64_t xin, int64_t epi, const Tensor& tiles, int64_t
   TORCH_CHECK(nb >= 1 && nb <= 8, "mg_gemv: batch columns must be 1..8");
   const int dev = tiles.device().index();
   const int sms = num_sms(dev);
-  TORCH_CHECK(part.is_cuda() && part.scalar_type() == at::kFloat && part.numel() >= (int64_t)sms * 2 * 8 * 2 * 32 * 4,
+  TORCH_CHECK(part.is_cuda() && part.scalar_type() == at::kFloat && part.numel() >= (int64_t)sms * 3 * 8 * 2 * 32 * 4,
               "mg_gemv: partial scratch too small");
   TORCH_CHECK(counters.is_cuda() && counters.scalar_type() == at::kInt && counters.numel() >= G,
               "mg_gemv: counters too small");

@@ -141,7 +141,7 @@ struct MgArgs {
   unsigned long long* const* push_recv;  // PUSH: as GemvArgs
   const int* push_epoch;
   int push_n;
-  // scratch: partial fragments [SMs * 2 CTAs * 8 warps][2][32] float4, zeroed counters [G]
+  // scratch: partial fragments [SMs * 3 CTAs * 8 warps][2][32] float4, zeroed counters [G]
   float4* part;
   int* counters;
   int* status;

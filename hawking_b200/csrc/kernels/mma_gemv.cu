@@ -8,9 +8,9 @@
 //    its A fragment for one k-step in one 32-bit word, four k-steps per 16-byte load). Tiles are
 //    stored row-group major, so any contiguous range of tiles is one contiguous byte range.
 //  * Streaming. The tiles are split into gridDim.x * 8 contiguous, equal ranges, one per warp (two
-//    CTAs of 8 warps per SM). Each
-//    warp owns a 4-deep ring of tile buffers in shared memory filled by cp.async.bulk (the TMA copy
-//    engine, completing on an mbarrier); lane 0 issues the first four copies before the
+//    or three CTAs of 8 warps per SM). Each
+//    warp owns a 3-deep ring of tile buffers in shared memory filled by cp.async.bulk (the TMA copy
+//    engine, completing on an mbarrier); lane 0 issues the first three copies before the
 //    programmatic-dependent-launch wait, so a kernel's weights stream in while the kernel before it
 //    finishes. No multicast (the kernel may run in multi-GPU processes).
 //  * Math. A nibble n becomes the bf16 value 1 + n/16 with one shift and one lop3 (the nibble lands
@@ -50,9 +50,9 @@ namespace mg {
 
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
-constexpr int kStages = 4;
+constexpr int kStages = 3;
 constexpr int kScaleBytes = 16 * 8 * 8;  // per warp: [16 rows][8 sub-blocks] float2 (S16, M'')
-constexpr int kMaxCtasPerSm = 2;         // resident CTAs per SM (the partial scratch is sized for this)
+constexpr int kMaxCtasPerSm = 3;         // resident CTAs per SM (the partial scratch is sized for this)
 
 template <int FMT> struct Tile;
 template <> struct Tile<WF_Q4_K> {
@@ -140,11 +140,12 @@ __device__ __forceinline__ void consume_q4k(const uint8_t* tile, int s, const XF
   for (int j = 0; j < 4; ++j) qv[j] = qp[j * 32];
   const bool has_col = n < nb;  // columns nb..NB-1 of the fragment are not staged: they read as 0
   const uint4* xp = x.p + (n * (int)x.cstride + s * 32 + q * 2);
-  uint4 xv[8];
+  // activations from global memory (long latency) are all requested up front; from shared memory
+  // they are loaded per k-step group, right before use (fewer live registers, more resident warps)
+  uint4 xv[XGLOBAL ? 8 : 2];
+  if constexpr (XGLOBAL) {
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    if (XGLOBAL) xv[j] = has_col ? __ldg(xp + (j >> 1) * 8 + (j & 1)) : make_uint4(0, 0, 0, 0);
-    else xv[j] = has_col ? xp[(j >> 1) * 8 + (j & 1)] : make_uint4(0, 0, 0, 0);
+    for (int j = 0; j < 8; ++j) xv[j] = has_col ? __ldg(xp + (j >> 1) * 8 + (j & 1)) : make_uint4(0, 0, 0, 0);
   }
   decode_scales_q4k(tile, scs, lane);
   __syncwarp();  // scales visible to every lane
@@ -152,9 +153,13 @@ __device__ __forceinline__ void consume_q4k(const uint8_t* tile, int s, const XF
   constexpr uint32_t M = 0x00780078u;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {  // k-step groups of 4 (two sub-blocks)
+    if constexpr (!XGLOBAL) {
+      xv[0] = has_col ? xp[j * 8] : make_uint4(0, 0, 0, 0);
+      xv[1] = has_col ? xp[j * 8 + 1] : make_uint4(0, 0, 0, 0);
+    }
 #pragma unroll
     for (int h = 0; h < 2; ++h) {  // sub-block 2j + h = k-steps 4j + 2h, 4j + 2h + 1
-      const uint4 b = xv[2 * j + h];
+      const uint4 b = XGLOBAL ? xv[(2 * j + h) % (XGLOBAL ? 8 : 2)] : xv[h];
       float c[4], e[4];
       {
         const uint32_t w = pick(qv[j], 2 * h);
@@ -287,7 +292,7 @@ __device__ __forceinline__ int pieces_of_group(uint32_t g, uint32_t KT, uint32_t
 }
 
 template <int FMT, int NB, int XIN, int EPI>
-__global__ void __launch_bounds__(kThreads, 2) mg_gemv_kernel(MgArgs a) {
+__global__ void __launch_bounds__(kThreads, kMaxCtasPerSm) mg_gemv_kernel(MgArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int TB = Tile<FMT>::BYTES;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -382,12 +387,15 @@ __global__ void __launch_bounds__(kThreads, 2) mg_gemv_kernel(MgArgs a) {
       int old = 0;
       if (lane == 0) old = atomicAdd(a.counters + g, 1);
       old = __shfl_sync(0xffffffffu, old, 0);
-      if (old == pieces_of_group(g, KT, T, P) - 1) {
+      // with T >= P no piece is empty: the contributors are exactly pf..pl
+      const bool dense = T >= P;
+      if (old == (dense ? (int)(pl - pf) : pieces_of_group(g, KT, T, P) - 1)) {
         __threadfence();
         float v[4] = {0.f, 0.f, 0.f, 0.f};
+        const int sl0 = (start_of(pf, T, P) / KT == g) ? 0 : 1;  // later pieces start inside g: slot 0
         // the contributing pieces in piece order (a fixed summation order); empty pieces skipped
-        for (uint32_t pp = pf;; pp = next_owner(pp, T, P)) {
-          const int sl = (start_of(pp, T, P) / KT == g) ? 0 : 1;
+        for (uint32_t pp = pf;; pp = dense ? pp + 1 : next_owner(pp, T, P)) {
+          const int sl = pp == pf ? sl0 : 0;
           const float4 pv = __ldcg(a.part + ((int64_t)pp * 2 + sl) * 32 + lane);
           v[0] += pv.x;
           v[1] += pv.y;

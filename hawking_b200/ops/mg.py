@@ -112,7 +112,7 @@ class MgScratch:
     def __init__(self, device, max_groups: int = 1 << 16):
         dev = torch.device(device)
         sms = kernels().mg_num_sms(dev.index or 0)
-        self.part = torch.zeros(sms * 2 * 8 * 2 * 32 * 4, dtype=torch.float32, device=dev)  # 2 CTAs of 8 warps per SM
+        self.part = torch.zeros(sms * 3 * 8 * 2 * 32 * 4, dtype=torch.float32, device=dev)  # 3 CTAs of 8 warps per SM
         self.counters = torch.zeros(max_groups, dtype=torch.int32, device=dev)
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
 
