@@ -86,8 +86,13 @@ __device__ __forceinline__ uint32_t pick(const uint4& v, int i) {
   return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
 }
 
-// Decode the 16 rows' Q4_K scales of one tile into per-warp shared memory: (S16, M'') for every
-// (row, sub-block). Lane t handles row t/2, sub-blocks 4*(t&1) .. +3.
+// Decode the 16 rows' Q4_K scales of one tile into per-warp shared memory. For sub-block k of a row
+// the contribution is S_k * c_k - M_k * e_k with S = 16 * d * sc, M = S + dmin * mn, c_k / e_k the
+// sub-block's sums of (1 + n/16) x and of x. The MMA accumulators run on across the tile's 8
+// sub-blocks (cumulative C_k, E_k: no zeroing per sub-block), so by Abel summation the tile adds
+// sum_k C_k (S_k - S_{k+1}) - E_k (M_k - M_{k+1}) with S_8 = M_8 = 0: the table holds those
+// differences. Lane t handles row t/2, sub-blocks 4*(t&1) .. +3; the first sub-block of the upper
+// half comes from the neighbouring lane.
 __device__ __forceinline__ void decode_scales_q4k(const uint8_t* tile, float2* scs, int lane) {
   const int row = lane >> 1, half = lane & 1;
   const uint4 h = *reinterpret_cast<const uint4*>(tile + row * 16);
@@ -98,21 +103,22 @@ __device__ __forceinline__ void decode_scales_q4k(const uint8_t* tile, float2* s
   const uint32_t mnb = half ? (((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u)) : (h.z & 0x3F3F3F3Fu);
   const float d16 = 16.f * d;
   const float c_sc = -d16 * 8388608.f, c_mn = -dmin * 8388608.f;
-  float v[8];
+  float S[5], M[5];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     // byte i placed in the mantissa of 2^23: the float 2^23 + byte, exact; one fma removes 2^23
     // and applies the scale with a single rounding
     const float scf = __uint_as_float(__byte_perm(scb, 0x4B000000u, 0x7650 + i));
     const float mnf = __uint_as_float(__byte_perm(mnb, 0x4B000000u, 0x7650 + i));
-    const float s16 = fmaf(d16, scf, c_sc);
-    const float mt = fmaf(dmin, mnf, c_mn);
-    v[2 * i] = s16;
-    v[2 * i + 1] = s16 + mt;
+    S[i] = fmaf(d16, scf, c_sc);
+    M[i] = S[i] + fmaf(dmin, mnf, c_mn);
   }
+  const float s_up = __shfl_down_sync(0xffffffffu, S[0], 1), m_up = __shfl_down_sync(0xffffffffu, M[0], 1);
+  S[4] = half ? 0.f : s_up;
+  M[4] = half ? 0.f : m_up;
   float4* dst = reinterpret_cast<float4*>(scs + row * 8 + half * 4);
-  dst[0] = make_float4(v[0], v[1], v[2], v[3]);
-  dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+  dst[0] = make_float4(S[0] - S[1], M[0] - M[1], S[1] - S[2], M[1] - M[2]);
+  dst[1] = make_float4(S[2] - S[3], M[2] - M[3], S[3] - S[4], M[3] - M[4]);
 }
 
 // 32-bit word index of the pair x[n][k], x[n][k + 1] (k even) in the B-fragment order. Column n
@@ -132,46 +138,43 @@ struct XFrag {
 template <int NB, bool XGLOBAL>
 __device__ __forceinline__ void consume_q4k(const uint8_t* tile, int s, const XFrag& x, int nb, float2* scs,
                                             int lane, float (&sum)[4]) {
-  const int n = lane >> 2, q = lane & 3, r0 = lane >> 2;
+  const int q = lane & 3, r0 = lane >> 2;
+  // lanes of batch columns beyond nb read column 0 (valid data; their outputs are discarded)
+  const int n = (lane >> 2) < nb ? (lane >> 2) : 0;
   // every load of the tile first (quants, activation fragments), so they are in flight together
   const uint4* qp = reinterpret_cast<const uint4*>(tile + 256) + lane;
   uint4 qv[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) qv[j] = qp[j * 32];
-  const bool has_col = n < nb;  // columns nb..NB-1 of the fragment are not staged: they read as 0
   const uint4* xp = x.p + (n * (int)x.cstride + s * 32 + q * 2);
   // activations from global memory (long latency) are all requested up front; from shared memory
   // they are loaded per k-step group, right before use (fewer live registers, more resident warps)
   uint4 xv[XGLOBAL ? 8 : 2];
   if constexpr (XGLOBAL) {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) xv[j] = has_col ? __ldg(xp + (j >> 1) * 8 + (j & 1)) : make_uint4(0, 0, 0, 0);
+    for (int j = 0; j < 8; ++j) xv[j] = __ldg(xp + (j >> 1) * 8 + (j & 1));
   }
   decode_scales_q4k(tile, scs, lane);
   __syncwarp();  // scales visible to every lane
   constexpr uint32_t ONES = 0x3F803F80u;
   constexpr uint32_t M = 0x00780078u;
+  float c[4] = {0.f, 0.f, 0.f, 0.f}, e[4] = {0.f, 0.f, 0.f, 0.f};  // cumulative over the tile
 #pragma unroll
   for (int j = 0; j < 4; ++j) {  // k-step groups of 4 (two sub-blocks)
     if constexpr (!XGLOBAL) {
-      xv[0] = has_col ? xp[j * 8] : make_uint4(0, 0, 0, 0);
-      xv[1] = has_col ? xp[j * 8 + 1] : make_uint4(0, 0, 0, 0);
+      xv[0] = xp[j * 8];
+      xv[1] = xp[j * 8 + 1];
     }
 #pragma unroll
     for (int h = 0; h < 2; ++h) {  // sub-block 2j + h = k-steps 4j + 2h, 4j + 2h + 1
       const uint4 b = XGLOBAL ? xv[(2 * j + h) % (XGLOBAL ? 8 : 2)] : xv[h];
-      float c[4], e[4];
-      {
-        const uint32_t w = pick(qv[j], 2 * h);
-        mma_bf16_z(c, and_or(w << 3, M, ONES), and_or(w >> 1, M, ONES), and_or(w >> 5, M, ONES),
-                   and_or(w >> 9, M, ONES), b.x, b.y);
-        mma_bf16_z(e, ONES, ONES, ONES, ONES, b.x, b.y);
-      }
-      {
-        const uint32_t w = pick(qv[j], 2 * h + 1);
+#pragma unroll
+      for (int kk = 0; kk < 2; ++kk) {
+        const uint32_t w = pick(qv[j], 2 * h + kk);
+        const uint32_t bx = kk ? b.z : b.x, by = kk ? b.w : b.y;
         mma_bf16(c, and_or(w << 3, M, ONES), and_or(w >> 1, M, ONES), and_or(w >> 5, M, ONES),
-                 and_or(w >> 9, M, ONES), b.z, b.w);
-        mma_bf16(e, ONES, ONES, ONES, ONES, b.z, b.w);
+                 and_or(w >> 9, M, ONES), bx, by);
+        mma_bf16(e, ONES, ONES, ONES, ONES, bx, by);
       }
       const int sb = 2 * j + h;
       const float2 s0 = scs[r0 * 8 + sb], s1 = scs[(r0 + 8) * 8 + sb];
@@ -359,9 +362,10 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm) mg_gemv_kernel(MgArgs
   bool ok = x_ok;  // a failed activation copy skips the tiles (the ring is drained below)
   uint32_t g = t0 / KT, s = t0 - g * KT;  // row group and column tile, advanced incrementally
   const uint32_t first_g = g;
-  for (; ok && i < n_tiles; ++i) {
-    const int st = i % kStages;
-    if (!sm100::mbar_wait(&bars[st], (uint32_t)((i / kStages) & 1), a.status)) {
+  int st = 0;
+  uint32_t phase = 0;
+  for (; ok && i < n_tiles; ++i, st = (st + 1 == kStages) ? 0 : st + 1, phase ^= (st == 0)) {
+    if (!sm100::mbar_wait(&bars[st], phase, a.status)) {
       ok = false;
       break;
     }
