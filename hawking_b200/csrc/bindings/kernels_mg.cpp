@@ -29,7 +29,7 @@ int num_sms(int dev) {
 
 // Pack Q4_K planes [quants (N, K/2), headers (N, K/16)] into tiles; rowmap int32 [G * 16].
 void mg_pack(int64_t fmt, const std::vector<Tensor>& planes, const Tensor& rowmap, int64_t G, int64_t KT,
-             const Tensor& out) {
+             const Tensor& out, int64_t math) {
   TORCH_CHECK(planes.size() == 2, "mg_pack: Q4_K expects [quants, headers] planes");
   TORCH_CHECK(rowmap.is_cuda() && rowmap.scalar_type() == at::kInt && rowmap.numel() == G * 16,
               "mg_pack: rowmap must be int32 [G * 16] on the device");
@@ -42,7 +42,7 @@ void mg_pack(int64_t fmt, const std::vector<Tensor>& planes, const Tensor& rowma
   w.p1 = ptr<const uint8_t>(planes[1]);
   w.rb1 = planes[1].stride(0);
   const c10::cuda::CUDAGuard g(out.device());
-  hk::mg_pack_launch((int)fmt, w, rowmap.data_ptr<int>(), (int)G, (int)KT, ptr<uint8_t>(out), cur_stream());
+  hk::mg_pack_launch((int)fmt, (int)math, w, rowmap.data_ptr<int>(), (int)G, (int)KT, ptr<uint8_t>(out), cur_stream());
 }
 
 void mg_gemv(int64_t fmt, int64_t xin, int64_t epi, const Tensor& tiles, int64_t G, int64_t KT, int64_t N, int64_t K,
@@ -51,7 +51,8 @@ void mg_gemv(int64_t fmt, int64_t xin, int64_t epi, const Tensor& tiles, int64_t
              const optional<Tensor>& y, const optional<Tensor>& bias, int64_t F, const optional<Tensor>& hfrag,
              int64_t hfrag_cstride, const optional<Tensor>& hb, const optional<Tensor>& argmax_slots,
              int64_t argmax_offset, const optional<Tensor>& push_recv, const optional<Tensor>& push_epoch,
-             const Tensor& part, const Tensor& counters, const Tensor& status, bool pdl) {
+             const Tensor& part, const Tensor& counters, const Tensor& status, bool pdl, int64_t math,
+             const optional<Tensor>& xinfo) {
   TORCH_CHECK(tiles.is_cuda() && tiles.is_contiguous(), "mg_gemv: tiles must be a contiguous CUDA tensor");
   TORCH_CHECK(tiles.numel() == G * KT * hk::mg_tile_bytes((int)fmt) && KT * 256 == K, "mg_gemv: tile shape mismatch");
   TORCH_CHECK(nb >= 1 && nb <= 8, "mg_gemv: batch columns must be 1..8");
@@ -91,6 +92,12 @@ void mg_gemv(int64_t fmt, int64_t xin, int64_t epi, const Tensor& tiles, int64_t
                 "mg_gemv: fragment-order input too small");
     a.xfrag = ptr<const uint4>(*xfrag);
     a.xfrag_cstride = xfrag_cstride;
+    if (math == hk::MG_MATH_INT) {
+      TORCH_CHECK(xinfo.has_value() && xinfo->is_cuda() && xinfo->scalar_type() == at::kFloat &&
+                      xinfo->numel() >= nb * (K / 32) * 2,
+                  "mg_gemv: integer fragment input needs its block info (fp32 [nb, K/32, 2])");
+      a.xinfo = reinterpret_cast<const float2*>(xinfo->data_ptr<float>());
+    }
   } else {
     TORCH_CHECK(false, "mg_gemv: bad input mode");
   }
@@ -129,15 +136,30 @@ void mg_gemv(int64_t fmt, int64_t xin, int64_t epi, const Tensor& tiles, int64_t
   a.part = reinterpret_cast<float4*>(part.data_ptr<float>());
   a.counters = counters.data_ptr<int>();
   a.status = status.data_ptr<int>();
+  a.math = (int)math;
   const c10::cuda::CUDAGuard g(tiles.device());
   hk::mg_gemv_launch((int)fmt, (int)xin, (int)epi, a, sms, cur_stream(), pdl);
+}
+void mg_quant(const Tensor& x, int64_t nb, int64_t K, const Tensor& xfrag, int64_t cstride, const Tensor& xinfo,
+              bool pdl) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.stride(-1) == 1 && x.size(0) >= nb &&
+                  x.size(1) >= K,
+              "mg_quant: x must be bf16 [nb, K]");
+  TORCH_CHECK(xfrag.is_cuda() && xfrag.numel() * xfrag.element_size() >= nb * cstride * 16, "mg_quant: xfrag too small");
+  TORCH_CHECK(xinfo.is_cuda() && xinfo.scalar_type() == at::kFloat && xinfo.numel() >= nb * (K / 32) * 2,
+              "mg_quant: xinfo too small");
+  const c10::cuda::CUDAGuard g(x.device());
+  hk::mg_quant_launch(ptr<const __nv_bfloat16>(x), x.stride(0), (int)nb, (int)K, ptr<uint4>(xfrag), cstride,
+                      reinterpret_cast<float2*>(xinfo.data_ptr<float>()), cur_stream(), pdl);
 }
 }  // namespace
 
 namespace hk {
 void register_mg_kernels(py::module_& m) {
   m.def("mg_pack", &mg_pack, py::arg("fmt"), py::arg("planes"), py::arg("rowmap"), py::arg("G"), py::arg("KT"),
-        py::arg("out"));
+        py::arg("out"), py::arg("math") = 0);
+  m.def("mg_quant", &mg_quant, py::arg("x"), py::arg("nb"), py::arg("K"), py::arg("xfrag"), py::arg("cstride"),
+        py::arg("xinfo"), py::arg("pdl") = false);
   m.def("mg_tile_bytes", &hk::mg_tile_bytes);
   m.def("mg_num_sms", [](int64_t dev) { return num_sms((int)dev); });
   m.def("mg_gemv", &mg_gemv, py::arg("fmt"), py::arg("xin"), py::arg("epi"), py::arg("tiles"), py::arg("G"),
@@ -147,6 +169,7 @@ void register_mg_kernels(py::module_& m) {
         py::arg("bias") = py::none(), py::arg("F") = 0, py::arg("hfrag") = py::none(),
         py::arg("hfrag_cstride") = 0, py::arg("hb") = py::none(), py::arg("argmax_slots") = py::none(),
         py::arg("argmax_offset") = 0, py::arg("push_recv") = py::none(), py::arg("push_epoch") = py::none(),
-        py::arg("part"), py::arg("counters"), py::arg("status"), py::arg("pdl") = false);
+        py::arg("part"), py::arg("counters"), py::arg("status"), py::arg("pdl") = false, py::arg("math") = 0,
+        py::arg("xinfo") = py::none());
 }
 }  // namespace hk

@@ -113,6 +113,11 @@ void gemv_launch(int fmt, int epi, const GemvArgs& a, int nb, cudaStream_t s, bo
 // activations, fp32 accumulation. See mma_gemv.cu for the design.
 enum MgInput : int { MG_X_NORM = 0, MG_X_BF16 = 1, MG_X_FRAG = 2, MG_X_FRAG_SMEM = 3 };  // 3: internal (FRAG staged)
 enum MgEpilogue : int { MG_STORE = 0, MG_RESID = 1, MG_SWIGLU = 2, MG_PUSH = 3 };
+// Math of the tiles: MG_MATH_BF16 (bf16 activations, bf16 MMA; tiles packed for it) or MG_MATH_INT
+// (activations as 16-bit fixed point per 32-element block, held as two int8 limbs, u8 x s8 MMA;
+// tiles packed for it). The input modes are the same; MG_X_FRAG of the integer math is the layout
+// written by mg_quant_launch.
+enum MgMath : int { MG_MATH_BF16 = 0, MG_MATH_INT = 1 };
 struct MgArgs {
   const uint8_t* tiles;     // [G row groups][KT column tiles][tile bytes]
   int G, KT;                // row groups (16 rows each), 256-column tiles per row group
@@ -126,7 +131,10 @@ struct MgArgs {
   const __nv_bfloat16* xb;  // MG_X_BF16: bf16 rows [nb, xb_stride]
   int64_t xb_stride;
   const uint4* xfrag;       // MG_X_FRAG: bf16 in B-fragment order, column n at n * xfrag_cstride uint4s
-  int64_t xfrag_cstride;
+  int64_t xfrag_cstride;    //   (integer math: the two limbs in B-fragment order, see mg_quant_launch)
+  const float2* xinfo;      // MG_X_FRAG, integer math: per (32-block b, column n) (d2, block sum) at
+                            //   xinfo[b * 8 + n]
+  int math;                 // MgMath of the tiles
   // outputs
   float* y;                 // STORE / RESID: fp32 [nb, y_stride]
   int64_t y_stride;
@@ -147,9 +155,14 @@ struct MgArgs {
   int* status;
 };
 int mg_tile_bytes(int fmt);
-size_t mg_smem_bytes(int fmt, int xin, int nb, int K);
+size_t mg_smem_bytes(int fmt, int math, int xin, int nb, int K);
 // rowmap[G * 16]: source row of each tile row (-1: zero row)
-void mg_pack_launch(int fmt, const WPlanes& w, const int* rowmap, int G, int KT, uint8_t* out, cudaStream_t s);
+void mg_pack_launch(int fmt, int math, const WPlanes& w, const int* rowmap, int G, int KT, uint8_t* out,
+                    cudaStream_t s);
+// Integer math, wide inputs: quantise bf16 rows [nb, x_stride] (K % 256 == 0) into the two-limb
+// B-fragment layout (column n at n * cstride uint4s) and the per-block info [K/32][8] float2.
+void mg_quant_launch(const __nv_bfloat16* x, int64_t x_stride, int nb, int K, uint4* xfrag, int64_t cstride,
+                     float2* xinfo, cudaStream_t s, bool pdl);
 void mg_gemv_launch(int fmt, int xin, int epi, const MgArgs& a, int sms, cudaStream_t s, bool pdl);
 
 // ---- decode ops (decode_ops.cu, attention.cu) ----

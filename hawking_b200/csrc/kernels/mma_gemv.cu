@@ -189,6 +189,171 @@ __device__ __forceinline__ void consume_q4k(const uint8_t* tile, int s, const XF
   __syncwarp();  // every lane is done with the tile and the scales before they are overwritten
 }
 
+// ---- integer math ------------------------------------------------------------------------------
+// Activations: per 32-element block b of column n, x_k ~= d2 * (254 * hi_k + lo_k) with
+// d1 = amax_b / 127, hi = round(x / d1), lo = round((x - hi d1) / d2), d2 = d1 / 254 (both limbs in
+// [-127, 127]): 16-bit fixed point per block, rounding error at most d2 / 2 = amax_b / 64516. The
+// block's (d2, sum of its represented values) goes with it.
+// Weight tiles (integer layout): per lane and sub-block two words; byte i of the first holds row
+// g's nibble of column 32 sb + 4q + i in its low half and row g + 8's in its high half (second
+// word: columns + 16). Masking yields the u8 A fragment of mma.m16n8k32 directly: rows g take
+// w & 0x0F0F0F0F (n), rows g + 8 take w & 0xF0F0F0F0 (16 n, their weight scale carries the 1/16).
+// One sub-block is one k32 MMA per limb; the integer dot 254 * dot_hi + dot_lo is exact.
+
+__device__ __forceinline__ void imma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%10,%10,%10};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
+// (S, M) per (row, sub-block): S = d * sc (rows 8..15: d * sc / 16), M = dmin * mn. Lane t handles
+// row t/2, sub-blocks 4*(t&1) .. +3.
+__device__ __forceinline__ void decode_scales_q4k_int(const uint8_t* tile, float2* scs, int lane) {
+  const int row = lane >> 1, half = lane & 1;
+  const uint4 h = *reinterpret_cast<const uint4*>(tile + row * 16);
+  float d = __half2float(__ushort_as_half((uint16_t)(h.x & 0xFFFF)));
+  const float dmin = __half2float(__ushort_as_half((uint16_t)(h.x >> 16)));
+  if (row >= 8) d *= 0.0625f;  // these rows enter the MMA as 16 n (exact)
+  const uint32_t scb = half ? ((h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u)) : (h.y & 0x3F3F3F3Fu);
+  const uint32_t mnb = half ? (((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u)) : (h.z & 0x3F3F3F3Fu);
+  const float c_sc = -d * 8388608.f, c_mn = -dmin * 8388608.f;
+  float v[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = fmaf(d, __uint_as_float(__byte_perm(scb, 0x4B000000u, 0x7650 + i)), c_sc);
+    v[2 * i + 1] = fmaf(dmin, __uint_as_float(__byte_perm(mnb, 0x4B000000u, 0x7650 + i)), c_mn);
+  }
+  float4* dst = reinterpret_cast<float4*>(scs + row * 8 + half * 4);
+  dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+  dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
+
+// Activation source of the integer math: limbs in B-fragment order (uint4 (hi.b0, hi.b1, lo.b0,
+// lo.b1) of lane quad q, block b, column n at n * cstride + b * 4 + q) and per (column, block)
+// float2 (d2, block sum) at n * istride + b.
+struct XInt {
+  const uint4* p;
+  int64_t cstride;
+  const float2* info;
+  int64_t istride;
+};
+
+template <int NB>
+__device__ __forceinline__ void consume_q4k_int(const uint8_t* tile, int s, const XInt& x, int nb, float2* scs,
+                                                int lane, float (&sum)[4]) {
+  const int q = lane & 3, r0 = lane >> 2;
+  const int n = (lane >> 2) < nb ? (lane >> 2) : 0;  // lanes beyond the batch read column 0
+  const uint4* qp = reinterpret_cast<const uint4*>(tile + 256) + lane;
+  uint4 qv[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) qv[j] = qp[j * 32];
+  decode_scales_q4k_int(tile, scs, lane);
+  __syncwarp();
+  const uint4* xp = x.p + (n * (int)x.cstride + s * 32 + q);
+  // columns 2q and 2q + 1 of the C fragment (clamped into the batch)
+  const int c0 = 2 * q < nb ? 2 * q : 0, c1 = 2 * q + 1 < nb ? 2 * q + 1 : 0;
+  const float2* ip0 = x.info + (c0 * (int)x.istride + s * 8);
+  const float2* ip1 = x.info + (c1 * (int)x.istride + s * 8);
+  constexpr uint32_t LO = 0x0F0F0F0Fu, HI = 0xF0F0F0F0u;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int sb = 2 * j + h;
+      const uint32_t w0 = pick(qv[j], 2 * h), w1 = pick(qv[j], 2 * h + 1);
+      const uint4 xb = xp[sb * 4];
+      int dh[4], dl[4];
+      imma_u8s8(dh, w0 & LO, w0 & HI, w1 & LO, w1 & HI, xb.x, xb.y);
+      imma_u8s8(dl, w0 & LO, w0 & HI, w1 & LO, w1 & HI, xb.z, xb.w);
+      const float2 s0 = scs[r0 * 8 + sb], s1 = scs[(r0 + 8) * 8 + sb];
+      const float2 i0 = ip0[sb];
+      sum[0] = fmaf(s0.x, i0.x * __int2float_rn(254 * dh[0] + dl[0]), fmaf(-s0.y, i0.y, sum[0]));
+      sum[2] = fmaf(s1.x, i0.x * __int2float_rn(254 * dh[2] + dl[2]), fmaf(-s1.y, i0.y, sum[2]));
+      if (NB > 1) {
+        const float2 i1 = ip1[sb];
+        sum[1] = fmaf(s0.x, i1.x * __int2float_rn(254 * dh[1] + dl[1]), fmaf(-s0.y, i1.y, sum[1]));
+        sum[3] = fmaf(s1.x, i1.x * __int2float_rn(254 * dh[3] + dl[3]), fmaf(-s1.y, i1.y, sum[3]));
+      }
+    }
+  }
+  __syncwarp();  // every lane is done with the tile and the scales before they are overwritten
+}
+
+// Quantise one 32-element block (one value per lane) into the two limbs; returns (d2, block sum)
+// and this lane's limbs.
+__device__ __forceinline__ float2 quant_block(float v, int& hi, int& lo) {
+  const float amax = warp_max(fabsf(v));
+  if (amax == 0.f) {
+    hi = lo = 0;
+    return make_float2(0.f, 0.f);
+  }
+  const float d1 = amax / 127.f, d2 = d1 / 254.f;
+  hi = max(-127, min(127, __float2int_rn(v / d1)));
+  const float r = fmaf(-(float)hi, d1, v);
+  lo = max(-127, min(127, __float2int_rn(r / d2)));
+  const float msum = warp_sum((float)(254 * hi + lo));  // |sum| < 2^24: exact
+  return make_float2(d2, d2 * msum);
+}
+// Byte offset of limb `limb` (0 hi, 1 lo) of element k of column n in the limb layout.
+__device__ __forceinline__ int64_t limb_byte(int n, int k, int64_t cstride, int limb) {
+  const int b = k >> 5, kk = k & 31;
+  return ((int64_t)n * cstride + b * 4 + ((kk & 15) >> 2)) * 16 + limb * 8 + (kk >> 4) * 4 + (kk & 3);
+}
+
+// Stage the activations of `nb` columns into shared memory as limbs + block info (integer math).
+template <int XIN>
+__device__ __forceinline__ void stage_x_int(const MgArgs& a, uint8_t* xs, int64_t cstride, float2* info,
+                                            int64_t istride, float* red) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, K = a.K, nblk = K / 32;
+  for (int n = 0; n < a.nb; ++n) {
+    float scale = 1.f;
+    if constexpr (XIN == MG_X_NORM) {
+      const float4* xr = reinterpret_cast<const float4*>(a.x_f32 + (int64_t)n * a.x_f32_stride);
+      float ss = 0.f;
+      for (int i = tid; i < K / 4; i += kThreads) {
+        const float4 v = xr[i];
+        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+      }
+      scale = rsqrtf(block_sum(ss, red) / (float)K + a.eps);
+    }
+    for (int b = warp; b < nblk; b += kWarps) {
+      const int k = 32 * b + lane;
+      float v;
+      if constexpr (XIN == MG_X_NORM) {
+        v = a.x_f32[(int64_t)n * a.x_f32_stride + k] * scale;
+        if (a.norm_w) v *= a.norm_w[k];
+      } else {
+        v = __bfloat162float(a.xb[(int64_t)n * a.xb_stride + k]);
+      }
+      int hi, lo;
+      const float2 inf = quant_block(v, hi, lo);
+      xs[limb_byte(n, k, cstride, 0)] = (uint8_t)(int8_t)hi;
+      xs[limb_byte(n, k, cstride, 1)] = (uint8_t)(int8_t)lo;
+      if (lane == 0) info[(int64_t)n * istride + b] = inf;
+    }
+  }
+  __syncthreads();
+}
+
+// Global two-limb quantiser (integer math, inputs too wide to stage): one warp per 32-block.
+__global__ void __launch_bounds__(256) quant_limbs_kernel(const __nv_bfloat16* x, int64_t x_stride, int nb, int K,
+                                                          uint8_t* out, int64_t cstride, float2* info) {
+  pdl_wait();
+  const int lane = threadIdx.x & 31, nblk = K / 32;
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (gw < nb * nblk) {
+    const int n = gw / nblk, b = gw - n * nblk, k = 32 * b + lane;
+    int hi, lo;
+    const float2 inf = quant_block(__bfloat162float(x[(int64_t)n * x_stride + k]), hi, lo);
+    out[limb_byte(n, k, cstride, 0)] = (uint8_t)(int8_t)hi;
+    out[limb_byte(n, k, cstride, 1)] = (uint8_t)(int8_t)lo;
+    if (lane == 0) info[(int64_t)n * nblk + b] = inf;
+  }
+  pdl_launch();
+}
+
 // Store the bf16 value of x[n][k] into a B-fragment-order buffer.
 __device__ __forceinline__ void frag_store_bf16(__nv_bfloat16* base, int64_t cstride, int n, int k, float v) {
   base[frag_u32(n, k & ~1, cstride) * 2 + (k & 1)] = __float2bfloat16_rn(v);
@@ -294,8 +459,8 @@ __device__ __forceinline__ int pieces_of_group(uint32_t g, uint32_t KT, uint32_t
   return n;
 }
 
-template <int FMT, int NB, int XIN, int EPI>
-__global__ void __launch_bounds__(kThreads, kMaxCtasPerSm) mg_gemv_kernel(MgArgs a) {
+template <int FMT, int MATH, int NB, int XIN, int EPI>
+__global__ void __launch_bounds__(kThreads, MATH == MG_MATH_INT ? 2 : kMaxCtasPerSm) mg_gemv_kernel(MgArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int TB = Tile<FMT>::BYTES;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -330,8 +495,34 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm) mg_gemv_kernel(MgArgs
   pdl_wait();
 
   XFrag x;
+  XInt xi;
   bool x_ok = true;
-  if constexpr (XIN == MG_X_FRAG_SMEM) {
+  if constexpr (MATH == MG_MATH_INT) {
+    const int64_t cs = (int64_t)a.K / 8 + 1;  // limbs: 2K bytes per column, one spare uint4 (bank spread)
+    const int64_t is = a.K / 32;
+    float2* info = reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(xs) + (int64_t)a.nb * cs * 16);
+    if constexpr (XIN == MG_X_FRAG_SMEM) {
+      uint64_t* xbar = reinterpret_cast<uint64_t*>(red);
+      if (threadIdx.x == 0) {
+        sm100::mbar_init(xbar, 1);
+        sm100::fence_barrier_init();
+        const uint32_t colb = (uint32_t)a.K * 2, infb = (uint32_t)is * 8;
+        sm100::mbar_arrive_expect_tx(xbar, (colb + infb) * (uint32_t)a.nb);
+        for (int n = 0; n < a.nb; ++n) {
+          sm100::bulk_g2s(xs + n * cs, a.xfrag + (int64_t)n * a.xfrag_cstride, colb, xbar);
+          sm100::bulk_g2s(info + n * is, a.xinfo + (int64_t)n * is, infb, xbar);
+        }
+      }
+      __syncthreads();
+      x_ok = sm100::mbar_wait(xbar, 0, a.status);
+      xi = XInt{xs, cs, info, is};
+    } else if constexpr (XIN == MG_X_FRAG) {
+      xi = XInt{a.xfrag, a.xfrag_cstride, a.xinfo, is};
+    } else {
+      stage_x_int<XIN>(a, reinterpret_cast<uint8_t*>(xs), cs, info, is, red);
+      xi = XInt{xs, cs, info, is};
+    }
+  } else if constexpr (XIN == MG_X_FRAG_SMEM) {
     // fragment-order activations copied into shared memory, one bulk copy per column (2K bytes)
     const int64_t cs = (int64_t)a.K / 64 * 8 + 1;
     uint64_t* xbar = reinterpret_cast<uint64_t*>(red);  // the reduction scratch is unused in this mode
@@ -369,7 +560,8 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm) mg_gemv_kernel(MgArgs
       ok = false;
       break;
     }
-    consume_q4k<NB, XIN == MG_X_FRAG>(ring + st * TB, (int)s, x, a.nb, scs, lane, sum);  // ends with __syncwarp
+    if constexpr (MATH == MG_MATH_INT) consume_q4k_int<NB>(ring + st * TB, (int)s, xi, a.nb, scs, lane, sum);
+    else consume_q4k<NB, XIN == MG_X_FRAG>(ring + st * TB, (int)s, x, a.nb, scs, lane, sum);  // both end with __syncwarp
     if (i + kStages < n_tiles) {
       if (lane == 0) {
         sm100::fence_proxy_async_smem();  // this stage's generic reads before the async overwrite
@@ -420,17 +612,19 @@ __global__ void __launch_bounds__(kThreads, kMaxCtasPerSm) mg_gemv_kernel(MgArgs
   }
 }
 
-size_t smem_bytes(int fmt, int xin, int nb, int K) {
+size_t smem_bytes(int fmt, int math, int xin, int nb, int K) {
   const size_t tb = (size_t)mg_tile_bytes(fmt);
   size_t s = kWarps * (kStages * tb + kScaleBytes) + kWarps * kStages * 8 + 128;
-  if (xin != MG_X_FRAG) s += (size_t)nb * ((size_t)K / 64 * 8 + 1) * 16;
-  (void)0;
+  if (xin != MG_X_FRAG) {
+    s += (size_t)nb * ((size_t)K / 8 + 1) * 16;                  // bf16 elements or the two int8 limbs
+    if (math == MG_MATH_INT) s += (size_t)nb * ((size_t)K / 32) * 8;  // per-block (d2, sum)
+  }
   return s;
 }
 
-template <int FMT, int XIN, int EPI>
+template <int FMT, int MATH, int XIN, int EPI>
 void dispatch_nb(const MgArgs& a, int sms, cudaStream_t st, bool pdl) {
-  const size_t smem = smem_bytes(FMT, XIN, a.nb, a.K);
+  const size_t smem = smem_bytes(FMT, MATH, XIN, a.nb, a.K);
   auto go = [&](auto kern) {
     HK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     int per_sm = 1;
@@ -438,26 +632,26 @@ void dispatch_nb(const MgArgs& a, int sms, cudaStream_t st, bool pdl) {
     per_sm = per_sm < 1 ? 1 : (per_sm > kMaxCtasPerSm ? kMaxCtasPerSm : per_sm);
     launch(kern, dim3(sms * per_sm), dim3(kThreads), smem, st, pdl, a);
   };
-  if (a.nb == 1) go(mg_gemv_kernel<FMT, 1, XIN, EPI>);
-  else if (a.nb == 2) go(mg_gemv_kernel<FMT, 2, XIN, EPI>);
-  else if (a.nb <= 4) go(mg_gemv_kernel<FMT, 4, XIN, EPI>);
-  else go(mg_gemv_kernel<FMT, 8, XIN, EPI>);
+  if (a.nb == 1) go(mg_gemv_kernel<FMT, MATH, 1, XIN, EPI>);
+  else if (a.nb == 2) go(mg_gemv_kernel<FMT, MATH, 2, XIN, EPI>);
+  else if (a.nb <= 4) go(mg_gemv_kernel<FMT, MATH, 4, XIN, EPI>);
+  else go(mg_gemv_kernel<FMT, MATH, 8, XIN, EPI>);
 }
 
-template <int FMT, int XIN>
+template <int FMT, int MATH, int XIN>
 void dispatch_epi(int epi, const MgArgs& a, int grid, cudaStream_t st, bool pdl) {
   switch (epi) {
-    case MG_STORE: dispatch_nb<FMT, XIN, MG_STORE>(a, grid, st, pdl); break;
-    case MG_RESID: dispatch_nb<FMT, XIN, MG_RESID>(a, grid, st, pdl); break;
-    case MG_SWIGLU: dispatch_nb<FMT, XIN, MG_SWIGLU>(a, grid, st, pdl); break;
-    case MG_PUSH: dispatch_nb<FMT, XIN, MG_PUSH>(a, grid, st, pdl); break;
+    case MG_STORE: dispatch_nb<FMT, MATH, XIN, MG_STORE>(a, grid, st, pdl); break;
+    case MG_RESID: dispatch_nb<FMT, MATH, XIN, MG_RESID>(a, grid, st, pdl); break;
+    case MG_SWIGLU: dispatch_nb<FMT, MATH, XIN, MG_SWIGLU>(a, grid, st, pdl); break;
+    case MG_PUSH: dispatch_nb<FMT, MATH, XIN, MG_PUSH>(a, grid, st, pdl); break;
     default: throw std::runtime_error("mg_gemv: bad epilogue");
   }
 }
 
 // ---- packing: GGUF Q4_K planes -> fragment-ordered tiles ------------------------------------
 __global__ void pack_q4k_kernel(const uint8_t* qs, int64_t rb0, const uint8_t* hdr, int64_t rb1, const int* rowmap,
-                                int G, int KT, uint32_t* out) {
+                                int G, int KT, uint32_t* out, int int_layout) {
   const int64_t total = (int64_t)G * KT * 576;  // 32-bit words per tile: 64 header + 512 quant
   for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
        idx += (int64_t)gridDim.x * blockDim.x) {
@@ -471,15 +665,26 @@ __global__ void pack_q4k_kernel(const uint8_t* qs, int64_t rb0, const uint8_t* h
                          : *reinterpret_cast<const uint32_t*>(hdr + (int64_t)src * rb1 + (int64_t)s * 16 + (w & 3) * 4);
       continue;
     }
-    const int qw = w - 64;  // ((ks >> 2) * 32 + t) * 4 + (ks & 3)
-    const int t = (qw >> 2) & 31, ks = (qw >> 7) * 4 + (qw & 3);
-    const int r0 = t >> 2, q = t & 3, e0 = 16 * ks + 2 * q;
-    const int s0 = rowmap[g * 16 + r0], s1 = rowmap[g * 16 + r0 + 8];
+    const int qw = w - 64;  // ((j * 32 + t) * 4 + e
+    const int t = (qw >> 2) & 31;
     auto nib = [&](int src, int e) -> uint32_t {
       if (src < 0) return 0u;
       const uint8_t b = qs[(int64_t)src * rb0 + (int64_t)s * 128 + 32 * (e >> 6) + (e & 31)];
       return (e & 32) ? (uint32_t)(b >> 4) : (uint32_t)(b & 15);
     };
+    if (int_layout) {  // integer math: sub-block 2j + e/2, word e&1; byte i = row g | row g+8 << 4
+      const int sb = (qw >> 7) * 2 + ((qw & 3) >> 1), word = qw & 1;
+      const int g8 = t >> 2, q = t & 3, k0 = 32 * sb + 16 * word + 4 * q;
+      const int s0 = rowmap[g * 16 + g8], s1 = rowmap[g * 16 + g8 + 8];
+      uint32_t v = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v |= (nib(s0, k0 + i) | (nib(s1, k0 + i) << 4)) << (8 * i);
+      out[idx] = v;
+      continue;
+    }
+    const int ks = (qw >> 7) * 4 + (qw & 3);
+    const int r0 = t >> 2, q = t & 3, e0 = 16 * ks + 2 * q;
+    const int s0 = rowmap[g * 16 + r0], s1 = rowmap[g * 16 + r0 + 8];
     out[idx] = nib(s0, e0) | nib(s0, e0 + 1) << 16 | nib(s1, e0) << 4 | nib(s1, e0 + 1) << 20 | nib(s0, e0 + 8) << 8 |
                nib(s0, e0 + 9) << 24 | nib(s1, e0 + 8) << 12 | nib(s1, e0 + 9) << 28;
   }
@@ -488,7 +693,7 @@ __global__ void pack_q4k_kernel(const uint8_t* qs, int64_t rb0, const uint8_t* h
 }  // namespace mg
 
 // Largest fragment-order activation block copied into shared memory (two CTAs per SM still fit).
-constexpr int64_t kFragSmemMax = 30 * 1024;
+constexpr int64_t kFragSmemMax = 34 * 1024;
 
 int mg_tile_bytes(int fmt) {
   switch (fmt) {
@@ -497,16 +702,42 @@ int mg_tile_bytes(int fmt) {
   }
 }
 
-size_t mg_smem_bytes(int fmt, int xin, int nb, int K) { return mg::smem_bytes(fmt, xin, nb, K); }
+size_t mg_smem_bytes(int fmt, int math, int xin, int nb, int K) { return mg::smem_bytes(fmt, math, xin, nb, K); }
 
-void mg_pack_launch(int fmt, const WPlanes& w, const int* rowmap, int G, int KT, uint8_t* out, cudaStream_t s) {
+void mg_pack_launch(int fmt, int math, const WPlanes& w, const int* rowmap, int G, int KT, uint8_t* out,
+                    cudaStream_t s) {
   if (fmt != WF_Q4_K) throw std::runtime_error("mg_pack: format not supported by the W4A16 GEMV");
   const int64_t total = (int64_t)G * KT * 576;
   const int threads = 256;
   const int blocks = (int)std::min<int64_t>((total + threads - 1) / threads, 65536);
   mg::pack_q4k_kernel<<<blocks, threads, 0, s>>>(w.p0, w.rb0, w.p1, w.rb1, rowmap, G, KT,
-                                                 reinterpret_cast<uint32_t*>(out));
+                                                 reinterpret_cast<uint32_t*>(out), math == MG_MATH_INT ? 1 : 0);
   HK_CUDA_CHECK(cudaGetLastError());
+}
+
+void mg_quant_launch(const __nv_bfloat16* x, int64_t x_stride, int nb, int K, uint4* xfrag, int64_t cstride,
+                     float2* xinfo, cudaStream_t s, bool pdl) {
+  if (K % 256 || nb < 1 || nb > 8 || cstride < K / 8) throw std::runtime_error("mg_quant: bad shape");
+  const int warps = nb * (K / 32);
+  launch(mg::quant_limbs_kernel, dim3((warps + 7) / 8), dim3(256), 0, s, pdl, x, x_stride, nb, K,
+         reinterpret_cast<uint8_t*>(xfrag), cstride, xinfo);
+}
+
+template <int MATH>
+static void dispatch_xin(int xin, int epi, const MgArgs& a, int sms, cudaStream_t s, bool pdl) {
+  switch (xin) {
+    case MG_X_NORM: mg::dispatch_epi<WF_Q4_K, MATH, MG_X_NORM>(epi, a, sms, s, pdl); break;
+    case MG_X_BF16: mg::dispatch_epi<WF_Q4_K, MATH, MG_X_BF16>(epi, a, sms, s, pdl); break;
+    case MG_X_FRAG: {
+      // stage the fragment-order activations in shared memory when they fit beside the rings
+      int64_t bytes = (int64_t)a.nb * (a.K / 8 + 1) * 16;
+      if (MATH == MG_MATH_INT) bytes += (int64_t)a.nb * (a.K / 32) * 8;
+      if (bytes <= kFragSmemMax) mg::dispatch_epi<WF_Q4_K, MATH, MG_X_FRAG_SMEM>(epi, a, sms, s, pdl);
+      else mg::dispatch_epi<WF_Q4_K, MATH, MG_X_FRAG>(epi, a, sms, s, pdl);
+      break;
+    }
+    default: throw std::runtime_error("mg_gemv: bad input mode");
+  }
 }
 
 void mg_gemv_launch(int fmt, int xin, int epi, const MgArgs& a, int sms, cudaStream_t s, bool pdl) {
@@ -514,7 +745,9 @@ void mg_gemv_launch(int fmt, int xin, int epi, const MgArgs& a, int sms, cudaStr
   if (a.nb < 1 || a.nb > 8) throw std::runtime_error("mg_gemv: batch columns must be 1..8");
   if (a.K % 256) throw std::runtime_error("mg_gemv: K must be a multiple of 256");
   if (xin == MG_X_NORM && a.K > 8192) throw std::runtime_error("mg_gemv: fused RMSNorm input needs K <= 8192");
-  if (xin != MG_X_FRAG && mg::smem_bytes(fmt, xin, a.nb, a.K) > 220 * 1024)
+  if (a.math != MG_MATH_BF16 && a.math != MG_MATH_INT) throw std::runtime_error("mg_gemv: bad math");
+  if (a.math == MG_MATH_INT && xin == MG_X_FRAG && !a.xinfo) throw std::runtime_error("mg_gemv: block info required");
+  if (xin != MG_X_FRAG && mg::smem_bytes(fmt, a.math, xin, a.nb, a.K) > 220 * 1024)
     throw std::runtime_error("mg_gemv: activations too wide to stage in shared memory (use the fragment input)");
   if (epi == MG_SWIGLU && !a.hfrag && !a.hb) throw std::runtime_error("mg_gemv swiglu: output buffer required");
   if ((epi == MG_STORE || epi == MG_RESID) && !a.y) throw std::runtime_error("mg_gemv: output y required");
@@ -524,18 +757,8 @@ void mg_gemv_launch(int fmt, int xin, int epi, const MgArgs& a, int sms, cudaStr
   if ((uint64_t)a.G * a.KT * ((uint64_t)sms * mg::kMaxCtasPerSm * mg::kWarps + 1) >= (1ull << 32))
     throw std::runtime_error("mg_gemv: matrix too large for 32-bit tile arithmetic");
   if ((int64_t)a.nb * (a.K / 64 * 8 + 1) >= (1ll << 31)) throw std::runtime_error("mg_gemv: activation index overflow");
-  switch (xin) {
-    case MG_X_NORM: mg::dispatch_epi<WF_Q4_K, MG_X_NORM>(epi, a, sms, s, pdl); break;
-    case MG_X_BF16: mg::dispatch_epi<WF_Q4_K, MG_X_BF16>(epi, a, sms, s, pdl); break;
-    case MG_X_FRAG:
-      // stage the fragment-order activations in shared memory when they fit beside the rings
-      if ((int64_t)a.nb * (a.K / 64 * 8 + 1) * 16 <= kFragSmemMax)
-        mg::dispatch_epi<WF_Q4_K, MG_X_FRAG_SMEM>(epi, a, sms, s, pdl);
-      else
-        mg::dispatch_epi<WF_Q4_K, MG_X_FRAG>(epi, a, sms, s, pdl);
-      break;
-    default: throw std::runtime_error("mg_gemv: bad input mode");
-  }
+  if (a.math == MG_MATH_INT) dispatch_xin<MG_MATH_INT>(xin, epi, a, sms, s, pdl);
+  else dispatch_xin<MG_MATH_BF16>(xin, epi, a, sms, s, pdl);
 }
 
 }  // namespace hk

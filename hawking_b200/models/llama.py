@@ -74,21 +74,21 @@ class LlamaWeights:
     rope_freqs: Optional[torch.Tensor] = None
     mg_head: Optional[object] = None
 
-    def prepare_mg(self):
+    def prepare_mg(self, math: str = "int"):
         """Re-lay every supported projection for the W4A16 small-batch GEMV (once; the planar
         GGUF copy stays for the tensor-core GEMM of prefill and large batches)."""
         for l in self.layers:
             if l.mg_qkv is None and len(l.wqkv) == 1 and mg.supported(l.wqkv[0]):
-                l.mg_qkv = mg.pack(l.wqkv[0])
+                l.mg_qkv = mg.pack(l.wqkv[0], math=math)
             if l.mg_o is None and mg.supported(l.wo):
-                l.mg_o = mg.pack(l.wo)
+                l.mg_o = mg.pack(l.wo, math=math)
             if l.moe is None and l.mg_gu is None and l.w_gu is not None and mg.supported(l.w_gu) \
-                    and l.w_gu.N == 2 * l.w_down.K and l.w_down.K % 64 == 0:
-                l.mg_gu = mg.pack(l.w_gu, swiglu=l.w_down.K)
+                    and l.w_gu.N == 2 * l.w_down.K and l.w_down.K % 256 == 0:
+                l.mg_gu = mg.pack(l.w_gu, swiglu=l.w_down.K, math=math)
             if l.moe is None and l.mg_down is None and mg.supported(l.w_down):
-                l.mg_down = mg.pack(l.w_down)
+                l.mg_down = mg.pack(l.w_down, math=math)
         if self.mg_head is None and mg.supported(self.lm_head):
-            self.mg_head = mg.pack(self.lm_head)
+            self.mg_head = mg.pack(self.lm_head, math=math)
 
     @property
     def mg_nbytes(self) -> int:
@@ -300,11 +300,15 @@ class LlamaModel:
         self.small_batch = os.environ.get("HK_SMALL_BATCH", "w4a16")
         if self.small_batch not in ("w4a16", "w4a8"):
             raise ValueError(f"HK_SMALL_BATCH must be w4a16 or w4a8, not {self.small_batch!r}")
+        # math of the W4A16 GEMV: "int" (activations as 16-bit fixed point per 32-element block on the
+        # integer tensor-core MMA, default) or "bf16" (activations rounded to bf16); ops/mg.py
+        self.mg_math = os.environ.get("HK_MG_MATH", "int")
         self.hfrag = None
         if self.small_batch == "w4a16":
-            weights.prepare_mg()
+            weights.prepare_mg(self.mg_math)
             if any(lw.mg_gu is not None for lw in weights.layers):
-                self.hfrag = mg.FragAct(max(lw.w_down.K for lw in weights.layers if lw.mg_gu is not None), self.dev)
+                Fm = max(lw.w_down.K for lw in weights.layers if lw.mg_gu is not None)
+                self.hfrag = mg.FragAct(Fm, self.dev) if self.mg_math == "bf16" else mg.IntFragAct(Fm, self.dev)
 
     def num_splits(self, rows: int) -> int:
         """KV splits per (row, kv head): the smallest power of two (at most 8, the portable
@@ -465,9 +469,26 @@ class LlamaModel:
             return
 
         def ffn(c0, c1):
-            mg.gemv(lw.mg_gu, c1 - c0, x_norm=(x[c0:c1], lw.ffn_norm, cfg.eps), hfrag=self.hfrag, status=st)
-            mg.gemv(lw.mg_down, c1 - c0, xfrag=self.hfrag, y=x[c0:c1], residual=True, status=st)
+            self._mg_ffn(lw, c1 - c0, dict(x_norm=(x[c0:c1], lw.ffn_norm, cfg.eps)), dict(y=x[c0:c1], residual=True))
         self._gemv_cols(ffn, rows)
+
+    def _mg_ffn(self, lw, nb, gu_in: dict, down_out: dict):
+        """gate/up + SwiGLU, then down, on the W4A16 GEMV. The bf16 math hands h over in fragment
+        order; the integer math writes h as bf16 rows, which the down GEMV quantises while staging
+        them (or, when too wide for shared memory, one quantiser launch writes its input layout)."""
+        st = self.status
+        F = lw.w_down.K
+        if self.mg_math == "bf16":
+            mg.gemv(lw.mg_gu, nb, hfrag=self.hfrag, status=st, **gu_in)
+            mg.gemv(lw.mg_down, nb, xfrag=self.hfrag, status=st, **down_out)
+            return
+        hb = self.hb[:nb, :F]
+        mg.gemv(lw.mg_gu, nb, hb=hb, status=st, **gu_in)
+        if nb * F * 2 <= 32 * 1024:
+            mg.gemv(lw.mg_down, nb, xb=hb, status=st, **down_out)
+        else:
+            mg.quantize(hb, nb, self.hfrag)
+            mg.gemv(lw.mg_down, nb, xfrag=self.hfrag, status=st, **down_out)
 
     def _attention_block_gemv(self, l, lw, rows, splits):
         x = self.x[:rows]
@@ -514,8 +535,7 @@ class LlamaModel:
             lw.moe.forward_ep(self, rows, 2 * l + 1)
         else:
             ops.tp_allreduce_rmsnorm_q8(tp, 2 * l, xa_res, xb_res, lw.ffn_norm, cfg.eps, out_bf16=self.xb[:rows])
-            mg.gemv(lw.mg_gu, rows, xb=self.xb[:rows], hfrag=self.hfrag, status=st)
-            mg.gemv(lw.mg_down, rows, xfrag=self.hfrag, push=(tp.push_recv[2 * l + 1], tp.epoch), status=st)
+            self._mg_ffn(lw, rows, dict(xb=self.xb[:rows]), dict(push=(tp.push_recv[2 * l + 1], tp.epoch)))
         nxt = w.layers[l + 1].attn_norm if l + 1 < len(w.layers) else w.out_norm
         q8, bf = self._tp_norm_out(l + 1, rows)
         ops.tp_allreduce_rmsnorm_q8(tp, 2 * l + 1, xb_res, xa_res, nxt, cfg.eps, q8, bf)

@@ -28,6 +28,10 @@ from .qweight import QWeight
 MG_X_NORM, MG_X_BF16, MG_X_FRAG = 0, 1, 2
 MG_STORE, MG_RESID, MG_SWIGLU, MG_PUSH = 0, 1, 2, 3
 MG_FORMATS = (GgmlType.Q4_K,)
+# Math of the packed tiles: "int" (default) takes each activation as 16-bit fixed point per
+# 32-element block (fp32 block scale; two int8 limbs on the u8 x s8 tensor-core MMA; rounding error
+# at most 1/64516 of the block's largest magnitude), "bf16" rounds activations to bf16 (bf16 MMA).
+MATHS = {"bf16": 0, "int": 1}
 
 
 @dataclass
@@ -39,6 +43,7 @@ class MgWeight:
     G: int          # row groups of 16 tile rows
     KT: int         # 256-column tiles per row group
     swiglu: bool = False
+    math: str = "int"
 
     @property
     def nbytes(self) -> int:
@@ -49,9 +54,12 @@ def supported(w: Optional[QWeight]) -> bool:
     return w is not None and w.fmt in MG_FORMATS and w.K % 256 == 0
 
 
-def pack(w: QWeight, swiglu: Optional[int] = None) -> MgWeight:
-    """Re-lay ``w`` (Q4_K) into fragment-ordered tiles. ``swiglu=F``: w is [gate (F rows) | up
-    (F rows)] and tile g holds gate rows 8g..8g+7 followed by the matching up rows."""
+def pack(w: QWeight, swiglu: Optional[int] = None, math: str = "int") -> MgWeight:
+    """Re-lay ``w`` (Q4_K) into fragment-ordered tiles for ``math`` ("int" or "bf16").
+    ``swiglu=F``: w is [gate (F rows) | up (F rows)] and tile g holds gate rows 8g..8g+7 followed by
+    the matching up rows."""
+    if math not in MATHS:
+        raise ValueError(f"mg.pack: math must be one of {sorted(MATHS)}")
     if not supported(w):
         raise ValueError(f"mg.pack: format {w.fmt} / K {w.K} not supported by the W4A16 GEMV")
     dev = w.device
@@ -72,8 +80,8 @@ def pack(w: QWeight, swiglu: Optional[int] = None) -> MgWeight:
         N = w.N
     KT = w.K // 256
     tiles = torch.empty(G * KT * kernels().mg_tile_bytes(int(w.fmt)), dtype=torch.uint8, device=dev)
-    kernels().mg_pack(int(w.fmt), w.planes, rowmap.to(torch.int32).to(dev), G, KT, tiles)
-    return MgWeight(tiles, int(w.fmt), N, w.K, G, KT, bool(swiglu))
+    kernels().mg_pack(int(w.fmt), w.planes, rowmap.to(torch.int32).to(dev), G, KT, tiles, math=MATHS[math])
+    return MgWeight(tiles, int(w.fmt), N, w.K, G, KT, bool(swiglu), math)
 
 
 def frag_index(K: int, nb: int, cstride: int, device) -> torch.Tensor:
@@ -100,6 +108,26 @@ class FragAct:
     def to_plain(self, nb: int) -> torch.Tensor:
         """[nb, K] bf16 in natural order (test helper)."""
         return self.buf.reshape(-1)[frag_index(self.K, nb, self.cstride, self.buf.device)].view(nb, self.K)
+
+
+class IntFragAct:
+    """Activations of up to 8 columns for the integer math, written by ``quantize``: two int8 limbs
+    per element in the tensor-core B-fragment order and per 32-element block (d2, block sum)."""
+
+    def __init__(self, K: int, device, cols: int = 8):
+        if K % 256:
+            raise ValueError("IntFragAct: K must be a multiple of 256")
+        self.K = K
+        self.buf = torch.zeros(cols, 2 * K, dtype=torch.uint8, device=device)
+        self.cstride = K // 8  # uint4s per column (2K bytes)
+        self.info = torch.zeros(cols, K // 32, 2, dtype=torch.float32, device=device)
+
+
+def quantize(x: torch.Tensor, nb: int, out: IntFragAct, pdl: Optional[bool] = None):
+    """bf16 rows [nb, K] -> the two-limb fragment layout of ``out`` (one launch)."""
+    from . import PDL, launches
+    launches.add()
+    kernels().mg_quant(x, nb, out.K, out.buf, out.cstride, out.info, PDL if pdl is None else pdl)
 
 
 class MgScratch:
@@ -133,13 +161,14 @@ class MgScratch:
 
 
 def gemv(mw: MgWeight, nb: int, *, x_norm=None, xb: Optional[torch.Tensor] = None,
-         xfrag: Optional[FragAct] = None, y: Optional[torch.Tensor] = None, residual: bool = False,
+         xfrag=None, y: Optional[torch.Tensor] = None, residual: bool = False,
          bias=None, hfrag: Optional[FragAct] = None, hb: Optional[torch.Tensor] = None, argmax_slots=None,
          argmax_offset: int = 0, push=None, status: Optional[torch.Tensor] = None, pdl: Optional[bool] = None,
          scratch: Optional[MgScratch] = None):
     """One W4A16 GEMV launch over ``nb`` batch columns.
 
-    ``x_norm=(x_f32, norm_w, eps)`` (norm_w may be None), ``xb`` or ``xfrag`` selects the input.
+    ``x_norm=(x_f32, norm_w, eps)`` (norm_w may be None), ``xb`` or ``xfrag`` (a ``FragAct`` for the
+    bf16 math, an ``IntFragAct`` for the integer math) selects the input.
     ``y`` with ``residual`` selects store / add; a SwiGLU-packed weight writes ``hfrag`` / ``hb``;
     ``push=(recv_table, epoch)`` selects the tensor-parallel push.
     """
@@ -170,4 +199,5 @@ def gemv(mw: MgWeight, nb: int, *, x_norm=None, xb: Optional[torch.Tensor] = Non
         hb=hb, argmax_slots=argmax_slots, argmax_offset=argmax_offset,
         push_recv=push[0] if push is not None else None, push_epoch=push[1] if push is not None else None,
         part=sc.part, counters=sc.counters, status=status if status is not None else sc.status,
-        pdl=PDL if pdl is None else pdl)
+        pdl=PDL if pdl is None else pdl, math=MATHS[mw.math],
+        xinfo=xfrag.info if isinstance(xfrag, IntFragAct) else None)
