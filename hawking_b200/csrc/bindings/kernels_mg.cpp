@@ -84,6 +84,9 @@ void mg_gemv(int64_t fmt, int64_t xin, int64_t epi, const Tensor& tiles, int64_t
                     xb->size(1) >= K && xb->stride(0) % 2 == 0 &&
                     reinterpret_cast<uintptr_t>(xb->data_ptr()) % 4 == 0,
                 "mg_gemv: xb must be bf16 [nb, K] with even row stride");
+    TORCH_CHECK(math != hk::MG_MATH_INT ||
+                    (xb->stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(xb->data_ptr()) % 16 == 0),
+                "mg_gemv: integer math reads xb rows with 16-byte loads (16-byte aligned rows required)");
     a.xb = ptr<const __nv_bfloat16>(*xb);
     a.xb_stride = xb->stride(0);
   } else if (xin == hk::MG_X_FRAG) {
@@ -143,8 +146,8 @@ void mg_gemv(int64_t fmt, int64_t xin, int64_t epi, const Tensor& tiles, int64_t
 void mg_quant(const Tensor& x, int64_t nb, int64_t K, const Tensor& xfrag, int64_t cstride, const Tensor& xinfo,
               bool pdl) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.stride(-1) == 1 && x.size(0) >= nb &&
-                  x.size(1) >= K,
-              "mg_quant: x must be bf16 [nb, K]");
+                  x.size(1) >= K && x.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0,
+              "mg_quant: x must be bf16 [nb, K] with 16-byte aligned rows");
   TORCH_CHECK(xfrag.is_cuda() && xfrag.numel() * xfrag.element_size() >= nb * cstride * 16, "mg_quant: xfrag too small");
   TORCH_CHECK(xinfo.is_cuda() && xinfo.scalar_type() == at::kFloat && xinfo.numel() >= nb * (K / 32) * 2,
               "mg_quant: xinfo too small");

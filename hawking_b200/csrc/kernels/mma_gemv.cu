@@ -281,32 +281,44 @@ __device__ __forceinline__ void consume_q4k_int(const uint8_t* tile, int s, cons
   __syncwarp();  // every lane is done with the tile and the scales before they are overwritten
 }
 
-// Quantise one 32-element block (one value per lane) into the two limbs; returns (d2, block sum)
-// and this lane's limbs.
-__device__ __forceinline__ float2 quant_block(float v, int& hi, int& lo) {
-  const float amax = warp_max(fabsf(v));
-  if (amax == 0.f) {
-    hi = lo = 0;
-    return make_float2(0.f, 0.f);
-  }
+// Quantise one 32-element block held by one thread into the two limbs, written as the block's 64
+// bytes of the limb layout (4 x 16 bytes at dst: lane quad q gets (hi k=4q.., hi k=16+4q..,
+// lo k=4q.., lo k=16+4q..)); returns (d2, sum of the represented values).
+__device__ __forceinline__ float2 quant_block_thread(const float (&v)[32], uint4* dst) {
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
   const float d1 = amax / 127.f, d2 = d1 / 254.f;
-  hi = max(-127, min(127, __float2int_rn(v / d1)));
-  const float r = fmaf(-(float)hi, d1, v);
-  lo = max(-127, min(127, __float2int_rn(r / d2)));
-  const float msum = warp_sum((float)(254 * hi + lo));  // |sum| < 2^24: exact
-  return make_float2(d2, d2 * msum);
-}
-// Byte offset of limb `limb` (0 hi, 1 lo) of element k of column n in the limb layout.
-__device__ __forceinline__ int64_t limb_byte(int n, int k, int64_t cstride, int limb) {
-  const int b = k >> 5, kk = k & 31;
-  return ((int64_t)n * cstride + b * 4 + ((kk & 15) >> 2)) * 16 + limb * 8 + (kk >> 4) * 4 + (kk & 3);
+  const float inv1 = amax > 0.f ? 127.f / amax : 0.f, inv2 = amax > 0.f ? 254.f * 127.f / amax : 0.f;
+  uint32_t hw[8], lw[8];
+  int msum = 0;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) {  // word w: elements 4w .. 4w+3
+    uint32_t hv = 0, lv = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float x = v[4 * w + i];
+      const int hi = max(-127, min(127, __float2int_rn(x * inv1)));
+      const int lo = max(-127, min(127, __float2int_rn(fmaf(-(float)hi, d1, x) * inv2)));
+      msum += 254 * hi + lo;
+      hv |= ((uint32_t)hi & 0xFFu) << (8 * i);
+      lv |= ((uint32_t)lo & 0xFFu) << (8 * i);
+    }
+    hw[w] = hv;
+    lw[w] = lv;
+  }
+#pragma unroll
+  for (int q = 0; q < 4; ++q) dst[q] = make_uint4(hw[q], hw[q + 4], lw[q], lw[q + 4]);
+  return make_float2(d2, d2 * (float)msum);
 }
 
-// Stage the activations of `nb` columns into shared memory as limbs + block info (integer math).
+// Stage the activations of `nb` columns into shared memory as limbs + block info (integer math):
+// each thread quantises whole 32-element blocks from registers (no cross-lane reductions).
 template <int XIN>
 __device__ __forceinline__ void stage_x_int(const MgArgs& a, uint8_t* xs, int64_t cstride, float2* info,
                                             int64_t istride, float* red) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, K = a.K, nblk = K / 32;
+  const int tid = threadIdx.x, K = a.K, nblk = K / 32;
+  uint4* xq = reinterpret_cast<uint4*>(xs);
   for (int n = 0; n < a.nb; ++n) {
     float scale = 1.f;
     if constexpr (XIN == MG_X_NORM) {
@@ -318,38 +330,60 @@ __device__ __forceinline__ void stage_x_int(const MgArgs& a, uint8_t* xs, int64_
       }
       scale = rsqrtf(block_sum(ss, red) / (float)K + a.eps);
     }
-    for (int b = warp; b < nblk; b += kWarps) {
-      const int k = 32 * b + lane;
-      float v;
+    for (int b = tid; b < nblk; b += kThreads) {
+      float v[32];
       if constexpr (XIN == MG_X_NORM) {
-        v = a.x_f32[(int64_t)n * a.x_f32_stride + k] * scale;
-        if (a.norm_w) v *= a.norm_w[k];
+        const float4* xr = reinterpret_cast<const float4*>(a.x_f32 + (int64_t)n * a.x_f32_stride + 32 * b);
+        const float4* wr = reinterpret_cast<const float4*>(a.norm_w + 32 * b);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 x4 = xr[i];
+          const float4 w4 = a.norm_w ? wr[i] : make_float4(1.f, 1.f, 1.f, 1.f);
+          v[4 * i] = x4.x * scale * w4.x;
+          v[4 * i + 1] = x4.y * scale * w4.y;
+          v[4 * i + 2] = x4.z * scale * w4.z;
+          v[4 * i + 3] = x4.w * scale * w4.w;
+        }
       } else {
-        v = __bfloat162float(a.xb[(int64_t)n * a.xb_stride + k]);
+        const uint4* xr = reinterpret_cast<const uint4*>(a.xb + (int64_t)n * a.xb_stride + 32 * b);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint4 u = xr[i];
+          const uint32_t ws[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            v[8 * i + 2 * j] = __uint_as_float(ws[j] << 16);
+            v[8 * i + 2 * j + 1] = __uint_as_float(ws[j] & 0xFFFF0000u);
+          }
+        }
       }
-      int hi, lo;
-      const float2 inf = quant_block(v, hi, lo);
-      xs[limb_byte(n, k, cstride, 0)] = (uint8_t)(int8_t)hi;
-      xs[limb_byte(n, k, cstride, 1)] = (uint8_t)(int8_t)lo;
-      if (lane == 0) info[(int64_t)n * istride + b] = inf;
+      info[(int64_t)n * istride + b] = quant_block_thread(v, xq + n * cstride + b * 4);
     }
   }
   __syncthreads();
 }
 
-// Global two-limb quantiser (integer math, inputs too wide to stage): one warp per 32-block.
+// Global two-limb quantiser (integer math, inputs too wide to stage): one thread per 32-block.
 __global__ void __launch_bounds__(256) quant_limbs_kernel(const __nv_bfloat16* x, int64_t x_stride, int nb, int K,
-                                                          uint8_t* out, int64_t cstride, float2* info) {
+                                                          uint4* out, int64_t cstride, float2* info) {
   pdl_wait();
-  const int lane = threadIdx.x & 31, nblk = K / 32;
-  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  if (gw < nb * nblk) {
-    const int n = gw / nblk, b = gw - n * nblk, k = 32 * b + lane;
-    int hi, lo;
-    const float2 inf = quant_block(__bfloat162float(x[(int64_t)n * x_stride + k]), hi, lo);
-    out[limb_byte(n, k, cstride, 0)] = (uint8_t)(int8_t)hi;
-    out[limb_byte(n, k, cstride, 1)] = (uint8_t)(int8_t)lo;
-    if (lane == 0) info[(int64_t)n * nblk + b] = inf;
+  const int nblk = K / 32;
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t < nb * nblk) {
+    const int n = t / nblk, b = t - n * nblk;
+    float v[32];
+    const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)n * x_stride + 32 * b);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint4 u = xr[i];
+      const uint32_t ws[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        v[8 * i + 2 * j] = __uint_as_float(ws[j] << 16);
+        v[8 * i + 2 * j + 1] = __uint_as_float(ws[j] & 0xFFFF0000u);
+      }
+    }
+    info[(int64_t)n * nblk + b] = quant_block_thread(v, out + n * cstride + b * 4);
   }
   pdl_launch();
 }
@@ -718,9 +752,9 @@ void mg_pack_launch(int fmt, int math, const WPlanes& w, const int* rowmap, int 
 void mg_quant_launch(const __nv_bfloat16* x, int64_t x_stride, int nb, int K, uint4* xfrag, int64_t cstride,
                      float2* xinfo, cudaStream_t s, bool pdl) {
   if (K % 256 || nb < 1 || nb > 8 || cstride < K / 8) throw std::runtime_error("mg_quant: bad shape");
-  const int warps = nb * (K / 32);
-  launch(mg::quant_limbs_kernel, dim3((warps + 7) / 8), dim3(256), 0, s, pdl, x, x_stride, nb, K,
-         reinterpret_cast<uint8_t*>(xfrag), cstride, xinfo);
+  const int warps = nb * (K / 32);  // one thread per block
+  launch(mg::quant_limbs_kernel, dim3((warps + 255) / 256), dim3(256), 0, s, pdl, x, x_stride, nb, K, xfrag,
+         cstride, xinfo);
 }
 
 template <int MATH>
