@@ -9,8 +9,8 @@
 //    stored row-group major, so any contiguous range of tiles is one contiguous byte range.
 //  * Streaming. The tiles are split into gridDim.x * 8 contiguous, equal ranges, one per warp (two
 //    or three CTAs of 8 warps per SM). Each
-//    warp owns a 3-deep ring of tile buffers in shared memory filled by cp.async.bulk (the TMA copy
-//    engine, completing on an mbarrier); lane 0 issues the first three copies before the
+//    warp owns a ring of 2 stages of 2 tiles in shared memory, each stage filled by one cp.async.bulk
+//    (the TMA copy engine, completing on an mbarrier); lane 0 issues the first copies before the
 //    programmatic-dependent-launch wait, so a kernel's weights stream in while the kernel before it
 //    finishes. No multicast (the kernel may run in multi-GPU processes).
 //  * Math. A nibble n becomes the bf16 value 1 + n/16 with one shift and one lop3 (the nibble lands
@@ -50,7 +50,8 @@ namespace mg {
 
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
-constexpr int kStages = 3;
+constexpr int kStages = 2;           // ring stages per warp
+constexpr int kTpc = 2;              // tiles per stage (one bulk copy each)
 constexpr int kScaleBytes = 16 * 8 * 8;  // per warp: [16 rows][8 sub-blocks] float2 (S16, M'')
 constexpr int kMaxCtasPerSm = 3;         // resident CTAs per SM (the partial scratch is sized for this)
 
@@ -281,43 +282,64 @@ __device__ __forceinline__ void consume_q4k_int(const uint8_t* tile, int s, cons
   __syncwarp();  // every lane is done with the tile and the scales before they are overwritten
 }
 
-// Quantise one 32-element block held by one thread into the two limbs, written as the block's 64
-// bytes of the limb layout (4 x 16 bytes at dst: lane quad q gets (hi k=4q.., hi k=16+4q..,
-// lo k=4q.., lo k=16+4q..)); returns (d2, sum of the represented values).
-__device__ __forceinline__ float2 quant_block_thread(const float (&v)[32], uint4* dst) {
+// Quantise one 32-element block held by a pair of adjacent lanes into the two limbs. Lane half h
+// holds v[0..7] = elements 8h .. 8h+7 and v[8..15] = elements 16+8h .. 16+8h+7, and writes lane quads
+// q = 2h, 2h+1 of the block's 64 bytes (uint4 q = (hi k=4q.., hi k=16+4q.., lo k=4q.., lo k=16+4q..)).
+// Rounding to the nearest integer is one fma against 1.5 * 2^23 (the integer lands in the low
+// mantissa bits, so its low byte is the int8 limb). Returns (d2, sum of the represented values).
+__device__ __forceinline__ uint32_t pack_low_bytes(float a, float b, float c, float d) {
+  const uint32_t ab = __byte_perm(__float_as_uint(a), __float_as_uint(b), 0x0040);
+  const uint32_t cd = __byte_perm(__float_as_uint(c), __float_as_uint(d), 0x0040);
+  return __byte_perm(ab, cd, 0x5410);
+}
+__device__ __forceinline__ float2 quant_half_block(const float (&v)[16], int h, uint4* dst) {
+  constexpr float MAGIC = 12582912.f;  // 1.5 * 2^23
   float amax = 0.f;
 #pragma unroll
-  for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
-  const float d1 = amax / 127.f, d2 = d1 / 254.f;
-  const float inv1 = amax > 0.f ? 127.f / amax : 0.f, inv2 = amax > 0.f ? 254.f * 127.f / amax : 0.f;
-  uint32_t hw[8], lw[8];
-  int msum = 0;
+  for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+  const float d1 = amax * (1.f / 127.f), d2 = d1 * (1.f / 254.f);
+  const float inv1 = amax > 0.f ? 127.f / amax : 0.f, inv2 = 254.f * inv1;
+  float th[16], tl[16], sh = 0.f, sl = 0.f;
 #pragma unroll
-  for (int w = 0; w < 8; ++w) {  // word w: elements 4w .. 4w+3
-    uint32_t hv = 0, lv = 0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float x = v[4 * w + i];
-      const int hi = max(-127, min(127, __float2int_rn(x * inv1)));
-      const int lo = max(-127, min(127, __float2int_rn(fmaf(-(float)hi, d1, x) * inv2)));
-      msum += 254 * hi + lo;
-      hv |= ((uint32_t)hi & 0xFFu) << (8 * i);
-      lv |= ((uint32_t)lo & 0xFFu) << (8 * i);
-    }
-    hw[w] = hv;
-    lw[w] = lv;
+  for (int i = 0; i < 16; ++i) {
+    th[i] = fmaf(v[i], inv1, MAGIC);
+    const float hf = th[i] - MAGIC;
+    tl[i] = fmaf(fmaf(-hf, d1, v[i]), inv2, MAGIC);
+    sh += hf;
+    sl += tl[i] - MAGIC;
   }
 #pragma unroll
-  for (int q = 0; q < 4; ++q) dst[q] = make_uint4(hw[q], hw[q + 4], lw[q], lw[q + 4]);
-  return make_float2(d2, d2 * (float)msum);
+  for (int qq = 0; qq < 2; ++qq)
+    dst[2 * h + qq] = make_uint4(pack_low_bytes(th[4 * qq], th[4 * qq + 1], th[4 * qq + 2], th[4 * qq + 3]),
+                                 pack_low_bytes(th[8 + 4 * qq], th[9 + 4 * qq], th[10 + 4 * qq], th[11 + 4 * qq]),
+                                 pack_low_bytes(tl[4 * qq], tl[4 * qq + 1], tl[4 * qq + 2], tl[4 * qq + 3]),
+                                 pack_low_bytes(tl[8 + 4 * qq], tl[9 + 4 * qq], tl[10 + 4 * qq], tl[11 + 4 * qq]));
+  float ms = fmaf(254.f, sh, sl);  // exact: integers below 2^24
+  ms += __shfl_xor_sync(0xffffffffu, ms, 1);
+  return make_float2(d2, d2 * ms);
+}
+
+// The 16 values of lane half h of block b of a bf16 row (elements 32b + 8h .., 32b + 16 + 8h ..).
+__device__ __forceinline__ void load_half_block_bf16(const __nv_bfloat16* row, int b, int h, float (&v)[16]) {
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    const uint4 u = *reinterpret_cast<const uint4*>(row + 32 * b + 16 * c + 8 * h);
+    const uint32_t ws[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      v[8 * c + 2 * j] = __uint_as_float(ws[j] << 16);
+      v[8 * c + 2 * j + 1] = __uint_as_float(ws[j] & 0xFFFF0000u);
+    }
+  }
 }
 
 // Stage the activations of `nb` columns into shared memory as limbs + block info (integer math):
-// each thread quantises whole 32-element blocks from registers (no cross-lane reductions).
+// each pair of threads quantises one 32-element block from registers.
 template <int XIN>
 __device__ __forceinline__ void stage_x_int(const MgArgs& a, uint8_t* xs, int64_t cstride, float2* info,
                                             int64_t istride, float* red) {
-  const int tid = threadIdx.x, K = a.K, nblk = K / 32;
+  const int tid = threadIdx.x, K = a.K, nblk = K / 32, h = tid & 1;
   uint4* xq = reinterpret_cast<uint4*>(xs);
   for (int n = 0; n < a.nb; ++n) {
     float scale = 1.f;
@@ -330,61 +352,54 @@ __device__ __forceinline__ void stage_x_int(const MgArgs& a, uint8_t* xs, int64_
       }
       scale = rsqrtf(block_sum(ss, red) / (float)K + a.eps);
     }
-    for (int b = tid; b < nblk; b += kThreads) {
-      float v[32];
-      if constexpr (XIN == MG_X_NORM) {
-        const float4* xr = reinterpret_cast<const float4*>(a.x_f32 + (int64_t)n * a.x_f32_stride + 32 * b);
-        const float4* wr = reinterpret_cast<const float4*>(a.norm_w + 32 * b);
+    // every lane of a warp runs the same number of iterations (the pair shuffles need both lanes)
+    for (int b0 = 0; b0 < nblk; b0 += kThreads / 2) {
+      const int b = b0 + (tid >> 1);
+      const bool on = b < nblk;
+      float v[16];
+      if (on) {
+        if constexpr (XIN == MG_X_NORM) {
+          const float* xr = a.x_f32 + (int64_t)n * a.x_f32_stride + 32 * b + 8 * h;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float4 x4 = xr[i];
-          const float4 w4 = a.norm_w ? wr[i] : make_float4(1.f, 1.f, 1.f, 1.f);
-          v[4 * i] = x4.x * scale * w4.x;
-          v[4 * i + 1] = x4.y * scale * w4.y;
-          v[4 * i + 2] = x4.z * scale * w4.z;
-          v[4 * i + 3] = x4.w * scale * w4.w;
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              const float4 x4 = *reinterpret_cast<const float4*>(xr + 16 * c + 4 * j);
+              const float4 w4 = a.norm_w ? *reinterpret_cast<const float4*>(a.norm_w + 32 * b + 8 * h + 16 * c + 4 * j)
+                                         : make_float4(1.f, 1.f, 1.f, 1.f);
+              v[8 * c + 4 * j] = x4.x * scale * w4.x;
+              v[8 * c + 4 * j + 1] = x4.y * scale * w4.y;
+              v[8 * c + 4 * j + 2] = x4.z * scale * w4.z;
+              v[8 * c + 4 * j + 3] = x4.w * scale * w4.w;
+            }
+        } else {
+          load_half_block_bf16(a.xb + (int64_t)n * a.xb_stride, b, h, v);
         }
       } else {
-        const uint4* xr = reinterpret_cast<const uint4*>(a.xb + (int64_t)n * a.xb_stride + 32 * b);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const uint4 u = xr[i];
-          const uint32_t ws[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            v[8 * i + 2 * j] = __uint_as_float(ws[j] << 16);
-            v[8 * i + 2 * j + 1] = __uint_as_float(ws[j] & 0xFFFF0000u);
-          }
-        }
+        for (int i = 0; i < 16; ++i) v[i] = 0.f;
       }
-      info[(int64_t)n * istride + b] = quant_block_thread(v, xq + n * cstride + b * 4);
+      uint4 scratch[4];
+      const float2 inf = quant_half_block(v, h, on ? xq + n * cstride + b * 4 : scratch);
+      if (on && h == 0) info[(int64_t)n * istride + b] = inf;
     }
   }
   __syncthreads();
 }
 
-// Global two-limb quantiser (integer math, inputs too wide to stage): one thread per 32-block.
+// Global two-limb quantiser (integer math, inputs too wide to stage): a lane pair per 32-block.
 __global__ void __launch_bounds__(256) quant_limbs_kernel(const __nv_bfloat16* x, int64_t x_stride, int nb, int K,
                                                           uint4* out, int64_t cstride, float2* info) {
   pdl_wait();
   const int nblk = K / 32;
-  const int t = blockIdx.x * blockDim.x + threadIdx.x;
-  if (t < nb * nblk) {
-    const int n = t / nblk, b = t - n * nblk;
-    float v[32];
-    const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)n * x_stride + 32 * b);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint4 u = xr[i];
-      const uint32_t ws[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        v[8 * i + 2 * j] = __uint_as_float(ws[j] << 16);
-        v[8 * i + 2 * j + 1] = __uint_as_float(ws[j] & 0xFFFF0000u);
-      }
-    }
-    info[(int64_t)n * nblk + b] = quant_block_thread(v, out + n * cstride + b * 4);
-  }
+  const int t = blockIdx.x * blockDim.x + threadIdx.x, h = t & 1, pb = t >> 1;
+  const bool on = pb < nb * nblk;
+  const int n = on ? pb / nblk : 0, b = on ? pb - n * nblk : 0;
+  float v[16];
+  load_half_block_bf16(x + (int64_t)n * x_stride, b, h, v);
+  uint4 scratch[4];
+  const float2 inf = quant_half_block(v, h, on ? out + n * cstride + b * 4 : scratch);
+  if (on && h == 0) info[(int64_t)n * nblk + b] = inf;
   pdl_launch();
 }
 
@@ -498,11 +513,11 @@ __global__ void __launch_bounds__(kThreads, MATH == MG_MATH_INT ? 2 : kMaxCtasPe
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int TB = Tile<FMT>::BYTES;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  uint8_t* ring = smem + warp * kStages * TB;
-  float2* scs = reinterpret_cast<float2*>(smem + kWarps * kStages * TB + warp * kScaleBytes);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kWarps * (kStages * TB + kScaleBytes)) + warp * kStages;
-  float* red = reinterpret_cast<float*>(smem + kWarps * (kStages * TB + kScaleBytes) + kWarps * kStages * 8);
-  uint4* xs = reinterpret_cast<uint4*>(smem + kWarps * (kStages * TB + kScaleBytes) + kWarps * kStages * 8 + 128);
+  uint8_t* ring = smem + warp * kStages * kTpc * TB;
+  float2* scs = reinterpret_cast<float2*>(smem + kWarps * kStages * kTpc * TB + warp * kScaleBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kWarps * (kStages * kTpc * TB + kScaleBytes)) + warp * kStages;
+  float* red = reinterpret_cast<float*>(smem + kWarps * (kStages * kTpc * TB + kScaleBytes) + kWarps * kStages * 8);
+  uint4* xs = reinterpret_cast<uint4*>(smem + kWarps * (kStages * kTpc * TB + kScaleBytes) + kWarps * kStages * 8 + 128);
 
   const uint32_t T = (uint32_t)a.G * (uint32_t)a.KT;
   const uint32_t P = gridDim.x * kWarps;
@@ -516,13 +531,16 @@ __global__ void __launch_bounds__(kThreads, MATH == MG_MATH_INT ? 2 : kMaxCtasPe
     sm100::fence_barrier_init();
   }
   __syncwarp();
-  auto issue = [&](int i) {
-    const int st = i % kStages;
-    sm100::mbar_arrive_expect_tx(&bars[st], TB);
-    sm100::bulk_g2s(ring + st * TB, a.tiles + (int64_t)(t0 + i) * TB, TB, &bars[st]);
+  // the warp's tiles stream in chunks of kTpc tiles, one bulk copy per chunk, kStages chunks ahead
+  const int n_chunks = (n_tiles + kTpc - 1) / kTpc;
+  auto issue = [&](int c) {
+    const int st = c % kStages;
+    const int cnt = min(kTpc, n_tiles - c * kTpc);
+    sm100::mbar_arrive_expect_tx(&bars[st], (uint32_t)(cnt * TB));
+    sm100::bulk_g2s(ring + st * kTpc * TB, a.tiles + (int64_t)(t0 + c * kTpc) * TB, (uint32_t)(cnt * TB), &bars[st]);
   };
   // weights first: they do not depend on the previous kernel
-  int issued = n_tiles < kStages ? n_tiles : kStages;  // same value on every lane
+  int issued = n_chunks < kStages ? n_chunks : kStages;  // chunks issued; same value on every lane
   if (lane == 0)
     for (int k = 0; k < issued; ++k) issue(k);
   pdl_launch();
@@ -587,21 +605,30 @@ __global__ void __launch_bounds__(kThreads, MATH == MG_MATH_INT ? 2 : kMaxCtasPe
   bool ok = x_ok;  // a failed activation copy skips the tiles (the ring is drained below)
   uint32_t g = t0 / KT, s = t0 - g * KT;  // row group and column tile, advanced incrementally
   const uint32_t first_g = g;
-  int st = 0;
+  int st = 0, u = 0, c = 0;  // stage, tile within the chunk, chunk
   uint32_t phase = 0;
-  for (; ok && i < n_tiles; ++i, st = (st + 1 == kStages) ? 0 : st + 1, phase ^= (st == 0)) {
-    if (!sm100::mbar_wait(&bars[st], phase, a.status)) {
+  for (; ok && i < n_tiles; ++i) {
+    if (u == 0 && !sm100::mbar_wait(&bars[st], phase, a.status)) {
       ok = false;
       break;
     }
-    if constexpr (MATH == MG_MATH_INT) consume_q4k_int<NB>(ring + st * TB, (int)s, xi, a.nb, scs, lane, sum);
-    else consume_q4k<NB, XIN == MG_X_FRAG>(ring + st * TB, (int)s, x, a.nb, scs, lane, sum);  // both end with __syncwarp
-    if (i + kStages < n_tiles) {
-      if (lane == 0) {
-        sm100::fence_proxy_async_smem();  // this stage's generic reads before the async overwrite
-        issue(i + kStages);
+    const uint8_t* tile = ring + (st * kTpc + u) * TB;
+    if constexpr (MATH == MG_MATH_INT) consume_q4k_int<NB>(tile, (int)s, xi, a.nb, scs, lane, sum);
+    else consume_q4k<NB, XIN == MG_X_FRAG>(tile, (int)s, x, a.nb, scs, lane, sum);  // both end with __syncwarp
+    if (++u == kTpc || i == n_tiles - 1) {  // chunk consumed: refill its stage
+      if (c + kStages < n_chunks) {
+        if (lane == 0) {
+          sm100::fence_proxy_async_smem();  // this stage's generic reads before the async overwrite
+          issue(c + kStages);
+        }
+        issued = c + kStages + 1;
       }
-      issued = i + kStages + 1;
+      u = 0;
+      ++c;
+      if (++st == kStages) {
+        st = 0;
+        phase ^= 1u;
+      }
     }
     const bool last = (i == n_tiles - 1) || (s == KT - 1);
     if (++s == KT) s = 0;
@@ -642,13 +669,13 @@ __global__ void __launch_bounds__(kThreads, MATH == MG_MATH_INT ? 2 : kMaxCtasPe
   }
   if (!ok && lane == 0) {
     // wait (bounded) for this warp's copies still in flight before the CTA may exit
-    for (int k = i; k < issued; ++k) sm100::mbar_wait(&bars[k % kStages], (uint32_t)((k / kStages) & 1), nullptr, 1u << 22);
+    for (int k = c; k < issued; ++k) sm100::mbar_wait(&bars[k % kStages], (uint32_t)((k / kStages) & 1), nullptr, 1u << 22);
   }
 }
 
 size_t smem_bytes(int fmt, int math, int xin, int nb, int K) {
   const size_t tb = (size_t)mg_tile_bytes(fmt);
-  size_t s = kWarps * (kStages * tb + kScaleBytes) + kWarps * kStages * 8 + 128;
+  size_t s = kWarps * (kStages * kTpc * tb + kScaleBytes) + kWarps * kStages * 8 + 128;
   if (xin != MG_X_FRAG) {
     s += (size_t)nb * ((size_t)K / 8 + 1) * 16;                  // bf16 elements or the two int8 limbs
     if (math == MG_MATH_INT) s += (size_t)nb * ((size_t)K / 32) * 8;  // per-block (d2, sum)
@@ -752,8 +779,8 @@ void mg_pack_launch(int fmt, int math, const WPlanes& w, const int* rowmap, int 
 void mg_quant_launch(const __nv_bfloat16* x, int64_t x_stride, int nb, int K, uint4* xfrag, int64_t cstride,
                      float2* xinfo, cudaStream_t s, bool pdl) {
   if (K % 256 || nb < 1 || nb > 8 || cstride < K / 8) throw std::runtime_error("mg_quant: bad shape");
-  const int warps = nb * (K / 32);  // one thread per block
-  launch(mg::quant_limbs_kernel, dim3((warps + 255) / 256), dim3(256), 0, s, pdl, x, x_stride, nb, K, xfrag,
+  const int threads = 2 * nb * (K / 32);  // a lane pair per block
+  launch(mg::quant_limbs_kernel, dim3((threads + 255) / 256), dim3(256), 0, s, pdl, x, x_stride, nb, K, xfrag,
          cstride, xinfo);
 }
 
