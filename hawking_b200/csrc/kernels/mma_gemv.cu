@@ -255,29 +255,49 @@ __device__ __forceinline__ void consume_q4k_int(const uint8_t* tile, int s, cons
   const uint4* xp = x.p + (n * (int)x.cstride + s * 32 + q);
   // columns 2q and 2q + 1 of the C fragment (clamped into the batch)
   const int c0 = 2 * q < nb ? 2 * q : 0, c1 = 2 * q + 1 < nb ? 2 * q + 1 : 0;
-  const float2* ip0 = x.info + (c0 * (int)x.istride + s * 8);
-  const float2* ip1 = x.info + (c1 * (int)x.istride + s * 8);
+  const float4* ip0 = reinterpret_cast<const float4*>(x.info + (c0 * (int)x.istride + s * 8));
+  const float4* ip1 = reinterpret_cast<const float4*>(x.info + (c1 * (int)x.istride + s * 8));
+  const float4* sp0 = reinterpret_cast<const float4*>(scs + r0 * 8);
+  const float4* sp1 = reinterpret_cast<const float4*>(scs + (r0 + 8) * 8);
   constexpr uint32_t LO = 0x0F0F0F0Fu, HI = 0xF0F0F0F0u;
+  // shared-memory operands of a pair of sub-blocks (2j, 2j+1): activation fragments, the rows'
+  // (S, M) and the columns' (d2, block sum), fetched together one pair ahead of their use
+  struct Ops {
+    uint4 x0, x1;
+    float4 s0, s1, i0, i1;
+  };
+  auto fetch = [&](int j, Ops& o) {
+    o.x0 = xp[(2 * j) * 4];
+    o.x1 = xp[(2 * j + 1) * 4];
+    o.s0 = sp0[j];
+    o.s1 = sp1[j];
+    o.i0 = ip0[j];
+    if (NB > 1) o.i1 = ip1[j];
+  };
+  Ops cur, nxt;
+  fetch(0, cur);
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
+    if (j < 3) fetch(j + 1, nxt);
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      const int sb = 2 * j + h;
       const uint32_t w0 = pick(qv[j], 2 * h), w1 = pick(qv[j], 2 * h + 1);
-      const uint4 xb = xp[sb * 4];
+      const uint4 xb = h ? cur.x1 : cur.x0;
       int dh[4], dl[4];
       imma_u8s8(dh, w0 & LO, w0 & HI, w1 & LO, w1 & HI, xb.x, xb.y);
       imma_u8s8(dl, w0 & LO, w0 & HI, w1 & LO, w1 & HI, xb.z, xb.w);
-      const float2 s0 = scs[r0 * 8 + sb], s1 = scs[(r0 + 8) * 8 + sb];
-      const float2 i0 = ip0[sb];
-      sum[0] = fmaf(s0.x, i0.x * __int2float_rn(254 * dh[0] + dl[0]), fmaf(-s0.y, i0.y, sum[0]));
-      sum[2] = fmaf(s1.x, i0.x * __int2float_rn(254 * dh[2] + dl[2]), fmaf(-s1.y, i0.y, sum[2]));
+      const float s0x = h ? cur.s0.z : cur.s0.x, s0y = h ? cur.s0.w : cur.s0.y;
+      const float s1x = h ? cur.s1.z : cur.s1.x, s1y = h ? cur.s1.w : cur.s1.y;
+      const float d20 = h ? cur.i0.z : cur.i0.x, x0 = h ? cur.i0.w : cur.i0.y;
+      sum[0] = fmaf(s0x, d20 * __int2float_rn(254 * dh[0] + dl[0]), fmaf(-s0y, x0, sum[0]));
+      sum[2] = fmaf(s1x, d20 * __int2float_rn(254 * dh[2] + dl[2]), fmaf(-s1y, x0, sum[2]));
       if (NB > 1) {
-        const float2 i1 = ip1[sb];
-        sum[1] = fmaf(s0.x, i1.x * __int2float_rn(254 * dh[1] + dl[1]), fmaf(-s0.y, i1.y, sum[1]));
-        sum[3] = fmaf(s1.x, i1.x * __int2float_rn(254 * dh[3] + dl[3]), fmaf(-s1.y, i1.y, sum[3]));
+        const float d21 = h ? cur.i1.z : cur.i1.x, x1 = h ? cur.i1.w : cur.i1.y;
+        sum[1] = fmaf(s0x, d21 * __int2float_rn(254 * dh[1] + dl[1]), fmaf(-s0y, x1, sum[1]));
+        sum[3] = fmaf(s1x, d21 * __int2float_rn(254 * dh[3] + dl[3]), fmaf(-s1y, x1, sum[3]));
       }
     }
+    if (j < 3) cur = nxt;
   }
   __syncwarp();  // every lane is done with the tile and the scales before they are overwritten
 }
