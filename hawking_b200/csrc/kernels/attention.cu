@@ -280,7 +280,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnDecodeArgs a) {
 }
 
 // ---------------------------------------------------------------------------------------------
-// Cluster variant: the S = num_splits CTAs of one (row, kv head) form a thread-block cluster; CTA s
+// Cluster variant: the S = num_splits (1..16) CTAs of one (row, kv head) form a thread-block cluster; CTA s
 // owns the s-th contiguous token range (a whole number of KV blocks). One thread streams the
 // range's K and V block slabs (block_size x head_dim bf16, contiguous per head) into shared
 // memory with untiled bulk async copies completing on an mbarrier: every byte of the window is in
@@ -501,9 +501,9 @@ __global__ void __launch_bounds__(WARPS * 32) attn_decode_cluster_kernel(AttnDec
   for (int blk = split + S * warp; blk < NBLK; blk += S * WARPS) {
     const int idx = blk * 32 + lane;
     const int g = idx / HD, d = idx % HD;
-    float mk[8], lk[8], okv[8];
+    float mk[16], lk[16], okv[16];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
+    for (int k = 0; k < 16; ++k) {
       if (k < S) {
         mk[k] = *cluster.map_shared_rank(&s_m[g], k);
         lk[k] = *cluster.map_shared_rank(&s_l[g], k);
@@ -512,13 +512,13 @@ __global__ void __launch_bounds__(WARPS * 32) attn_decode_cluster_kernel(AttnDec
     }
     float M = -INFINITY;
 #pragma unroll
-    for (int k = 0; k < 8; ++k)
+    for (int k = 0; k < 16; ++k)
       if (k < S) M = fmaxf(M, mk[k]);
     const float sink = a.sinks ? a.sinks[kvh * G + g] : -INFINITY;
     M = fmaxf(M, sink);
     float L = 0.f, O = 0.f;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
+    for (int k = 0; k < 16; ++k) {
       if (k < S && mk[k] != -INFINITY) {
         const float f = __expf(mk[k] - M);
         L += lk[k] * f;
@@ -562,6 +562,8 @@ static void launch_cluster_g(AttnDecodeArgs a, cudaStream_t s, bool pdl) {
   const size_t smem = 128 + (size_t)ns * pair;
   auto kern = attn_decode_cluster_kernel<G, HPL, WARPS>;
   HK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  // 16-CTA clusters (splits of one (row, kv head)) need the non-portable size (sm_90+)
+  if (a.num_splits > 8) HK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
   launch_cluster(kern, dim3(a.num_splits, a.nkv, a.R), dim3(WARPS * 32), smem, s, pdl, a.num_splits, a);
 }
 
@@ -583,8 +585,8 @@ void attention_decode_cluster_launch(const AttnDecodeArgs& a, cudaStream_t s, bo
   if (a.nh % a.nkv) throw std::runtime_error("attention: n_heads must be a multiple of n_kv_heads");
   if ((reinterpret_cast<uintptr_t>(a.k_cache) | reinterpret_cast<uintptr_t>(a.v_cache)) & 15)
     throw std::runtime_error("attention (cluster): K/V caches must be 16-byte aligned");
-  if (a.num_splits != 1 && a.num_splits != 2 && a.num_splits != 4 && a.num_splits != 8)
-    throw std::runtime_error("attention (cluster): num_splits must be 1, 2, 4 or 8");
+  if (a.num_splits != 1 && a.num_splits != 2 && a.num_splits != 4 && a.num_splits != 8 && a.num_splits != 16)
+    throw std::runtime_error("attention (cluster): num_splits must be 1, 2, 4, 8 or 16");
   const int G = a.nh / a.nkv;
   switch (a.hd) {
     case 64: launch_cluster_hpl<2>(a, G, s, pdl); break;

@@ -186,12 +186,12 @@ def attention_decode(q, k_cache, v_cache, block_tables, row_seq, row_ctx, scale,
                      cluster: Optional[bool] = None):
     """Split-KV paged decode attention.
 
-    Cluster path (default when num_splits is 1, 2, 4 or 8): the splits of one (row, kv head) are a
+    Cluster path (default when num_splits is 1, 2, 4, 8 or 16): the splits of one (row, kv head) are a
     thread-block cluster and merge through distributed shared memory; no scratch is touched.
     Scratch path: the per-split partials go to part_o / part_lse with the zero-initialised int32
     ``counters`` [rows * n_kv_heads]; the last split CTA of each (row, kv head) merges them."""
     if cluster is None:
-        cluster = num_splits in (1, 2, 4, 8)
+        cluster = num_splits in (1, 2, 4, 8, 16)
     launches.add(1)
     kernels().attention_decode(q, k_cache, v_cache, block_tables, row_seq, row_ctx, scale, num_splits, part_o,
                                part_lse, out, out_q8.q if out_q8 else None, out_q8.d if out_q8 else None,
