@@ -311,14 +311,15 @@ class LlamaModel:
                 self.hfrag = mg.FragAct(Fm, self.dev) if self.mg_math == "bf16" else mg.IntFragAct(Fm, self.dev)
 
     def num_splits(self, rows: int) -> int:
-        """KV splits per (row, kv head): the smallest power of two (at most 16, the largest
-        thread-block cluster) that puts at least one CTA on every SM. ``force_splits``
+        """KV splits per (row, kv head): the smallest power of two (at most 8, the portable
+        thread-block cluster size; 16-CTA clusters measured slower) that puts at least one CTA on
+        every SM. ``force_splits``
         overrides it (speculative verify uses the single-row split so its logits are bitwise those
         of plain greedy decode)."""
         if self.force_splits:
             return self.force_splits
         s = 1
-        while s < min(16, self.max_splits) and rows * self.cfg.n_kv_heads * s < 148:
+        while s < min(8, self.max_splits) and rows * self.cfg.n_kv_heads * s < 148:
             s *= 2
         return s
 

@@ -132,3 +132,65 @@ def test_tp2_expert_parallel_moe_matches_tp1(shared, tmp_path):
     mp.spawn(_moe_worker, args=(2, _free_port(), shared, out), nprocs=2, join=True)
     r = torch.load(out)
     assert r["err"] < 0.03, r
+
+
+def _dense_q4k_worker(rank, world, port, math, out_path):
+    """Q4_K dense Llama shape: the decode path runs the W4A16 GEMV with its push epilogue."""
+    import datetime
+
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    os.environ["HK_MG_MATH"] = math
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        from hawking_b200.engine.engine import Engine
+        from hawking_b200.engine.sampling import SamplingParams
+        from hawking_b200.models.config import preset
+        from hawking_b200.models.llama import random_llama_weights
+        from hawking_b200.parallel.tp import TPComm, local_config, shard_llama_weights
+        cfg = preset("llama3-8b", layers=2, hidden=1024, n_heads=8, n_kv_heads=2, ffn=2048, vocab=2048, max_ctx=128)
+        w = random_llama_weights(cfg, dev, seed=5, std=0.05)  # same seed: identical on every rank
+        tp = TPComm(rank, world, 2 * cfg.layers, 8, cfg.hidden, dev)
+        eng = Engine.build(local_config(cfg, world), shard_llama_weights(w, cfg, rank, world), device=dev,
+                           max_batch=4, max_ctx=128, block_size=16, num_blocks=64, max_rows=8, tp=tp)
+        assert eng.model._mg_layer(eng.model.w.layers[0])
+        toks = list(range(10, 16))  # <= 8 rows: the GEMV path with the push all-reduce
+        local = eng.model.forward_tokens(toks, seq_id=1)
+        eng.kv.drop(1)
+        parts = [torch.empty_like(local) for _ in range(world)]
+        dist.all_gather(parts, local.contiguous())
+        full = torch.cat(parts, 1)
+        gen = eng.generate([list(range(30, 40)), list(range(50, 53))], SamplingParams(max_tokens=5))
+        gens = [None] * world
+        dist.all_gather_object(gens, gen)
+        tp.check()
+        if rank == 0:
+            ref = Engine.build(cfg, w, device=dev, max_batch=4, max_ctx=128, block_size=16, num_blocks=64,
+                               max_rows=8)
+            ref_logits = ref.model.forward_tokens(toks, seq_id=1)
+            ref.kv.drop(1)
+            ref_gen = ref.generate([list(range(30, 40)), list(range(50, 53))], SamplingParams(max_tokens=5))
+            err = float((full - ref_logits).abs().max() / ref_logits.abs().max())
+            torch.save({"err": err, "gens": gens, "ref_gen": ref_gen}, out_path)
+        torch.cuda.synchronize()
+        tp.close()
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("math", ["int", "bf16"])
+def test_tp2_q4k_w4a16_push_matches_tp1(math, tmp_path):
+    import torch.multiprocessing as mp
+    out = str(tmp_path / "dense.pt")
+    mp.spawn(_dense_q4k_worker, args=(2, _free_port(), math, out), nprocs=2, join=True)
+    r = torch.load(out)
+    assert r["err"] < 0.01, r
+    assert r["gens"][0] == r["gens"][1]  # every rank decodes the same tokens
+    assert [g[0] for g in r["gens"][0]] == [g[0] for g in r["ref_gen"]], r
