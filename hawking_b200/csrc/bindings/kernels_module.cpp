@@ -183,7 +183,7 @@ void attention_decode(const Tensor& q, const Tensor& k_cache, const Tensor& v_ca
                       const Tensor& part_o, const Tensor& part_lse, const optional<Tensor>& out,
                       const optional<Tensor>& oq, const optional<Tensor>& od, const optional<Tensor>& os,
                       const optional<Tensor>& sinks, const optional<Tensor>& out_bf16,
-                      const optional<Tensor>& counters, bool pdl, bool cluster) {
+                      const optional<Tensor>& counters, bool pdl, bool cluster, bool tc, const optional<Tensor>& status) {
   check_cuda(q, "q");
   TORCH_CHECK(q.dim() == 3 && q.scalar_type() == at::kFloat, "q must be fp32 [R, nh, hd]");
   TORCH_CHECK(k_cache.dim() == 4 && k_cache.scalar_type() == at::kBFloat16, "k_cache must be bf16 [blocks, nkv, bs, hd]");
@@ -218,9 +218,16 @@ void attention_decode(const Tensor& q, const Tensor& k_cache, const Tensor& v_ca
   a.out_bf16 = optr<__nv_bfloat16>(out_bf16);
   a.counters = optr<int>(counters);
   TORCH_CHECK(!counters.has_value() || counters->numel() >= (int64_t)R * a.nkv, "attention: counters too small");
+  a.status = optr<int>(status);
   const c10::cuda::CUDAGuard g(q.device());
-  if (cluster) hk::attention_decode_cluster_launch(a, cur_stream(), pdl);
-  else hk::attention_decode_launch(a, cur_stream(), pdl);
+  if (tc && hk::attention_decode_tc_supported(a)) {
+    TORCH_CHECK(k_cache.is_contiguous() && v_cache.is_contiguous(), "attention (tensor cores): contiguous caches");
+    hk::attention_decode_tc_launch(a, k_cache.numel() / hd, cur_stream(), pdl);
+  } else if (cluster) {
+    hk::attention_decode_cluster_launch(a, cur_stream(), pdl);
+  } else {
+    hk::attention_decode_launch(a, cur_stream(), pdl);
+  }
 }
 
 void attention_prefill(const Tensor& q, const Tensor& k_cache, const Tensor& v_cache, const Tensor& block_tables,
@@ -331,7 +338,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("part_o"), py::arg("part_lse"), py::arg("out") = py::none(), py::arg("oq") = py::none(),
         py::arg("od") = py::none(), py::arg("os") = py::none(), py::arg("sinks") = py::none(),
         py::arg("out_bf16") = py::none(), py::arg("counters") = py::none(), py::arg("pdl") = false,
-        py::arg("cluster") = false);
+        py::arg("cluster") = false, py::arg("tc") = false, py::arg("status") = py::none());
   m.def("argmax", &argmax, py::arg("logits"), py::arg("out"), py::arg("pdl") = false);
   m.def(
       "argmax_finalize",

@@ -223,6 +223,11 @@ void attention_decode_launch(const AttnDecodeArgs& a, cudaStream_t s, bool pdl);
 // Cluster variant (num_splits in {1, 2, 4, 8}): the splits of one (row, kv head) merge through
 // distributed shared memory; part_o / part_lse / counters are not used.
 void attention_decode_cluster_launch(const AttnDecodeArgs& a, cudaStream_t s, bool pdl);
+// Tensor-core decode (attention_tc.cu): TMA tensor loads of the K/V blocks, query heads of a KV head
+// as MMA rows, splits in a cluster (num_splits 1, 2, 4 or 8). cache_rows = num_blocks * nkv *
+// block_size (the rows of the caches viewed as [rows, hd]). head_dim 64 or 128, GQA group <= 16.
+bool attention_decode_tc_supported(const AttnDecodeArgs& a);
+void attention_decode_tc_launch(const AttnDecodeArgs& a, int64_t cache_rows, cudaStream_t s, bool pdl);
 // Causal prefill on the tensor cores (attention_prefill.cu): any rows (runs of one sequence are
 // found on the device), head_dim 64 or 128; outputs out / out_bf16 / q8 (split fields unused).
 void attention_prefill_launch(const AttnDecodeArgs& a, cudaStream_t s, bool pdl);

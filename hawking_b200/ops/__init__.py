@@ -181,9 +181,14 @@ def advance(ids, next_ids, positions, row_ctx, rows: int):
     kernels().advance(ids, next_ids, positions, row_ctx, rows, PDL)
 
 
+# Decode attention on the tensor cores (attention_tc.cu) where the shape allows it (head_dim 64 / 128,
+# GQA group <= 16, block size 16 / 32 / 64, splits 1-8); HK_ATTN_TC=0 selects the CUDA-core kernels.
+ATTN_TC = os.environ.get("HK_ATTN_TC", "1") == "1"
+
+
 def attention_decode(q, k_cache, v_cache, block_tables, row_seq, row_ctx, scale, num_splits, part_o, part_lse,
                      out=None, out_q8: Optional[Q8Act] = None, sinks=None, out_bf16=None, counters=None,
-                     cluster: Optional[bool] = None):
+                     cluster: Optional[bool] = None, tc: Optional[bool] = None, status=None):
     """Split-KV paged decode attention.
 
     Cluster path (default when num_splits is 1, 2, 4, 8 or 16): the splits of one (row, kv head) are a
@@ -195,7 +200,8 @@ def attention_decode(q, k_cache, v_cache, block_tables, row_seq, row_ctx, scale,
     launches.add(1)
     kernels().attention_decode(q, k_cache, v_cache, block_tables, row_seq, row_ctx, scale, num_splits, part_o,
                                part_lse, out, out_q8.q if out_q8 else None, out_q8.d if out_q8 else None,
-                               out_q8.s if out_q8 else None, sinks, out_bf16, counters, PDL, cluster)
+                               out_q8.s if out_q8 else None, sinks, out_bf16, counters, PDL, cluster,
+                               tc=(ATTN_TC if tc is None else tc) and cluster, status=status)
 
 
 def attention_prefill(q, k_cache, v_cache, block_tables, row_seq, row_ctx, scale, out=None,
