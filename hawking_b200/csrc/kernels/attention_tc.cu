@@ -7,9 +7,11 @@
 //    stages with TMA tensor loads (cp.async.bulk.tensor, 128-byte swizzle, no multicast): each
 //    stage holds one block's K and V as boxes of [block_size tokens x 64 dims]. The swizzle makes
 //    the ldmatrix reads below bank-conflict free.
-//  * Math. Consumer warps take 16-token units. S = Q K^T: the scaled bf16 query fragments stay in
-//    registers, K fragments come from ldmatrix (HD / 16 k-steps x 2 token tiles). Online softmax in
-//    the log2 domain on the accumulator fragments (row statistics over the four lanes of a quad).
+//  * Math. Consumer warps take 16-token units. S = Q K^T: the bf16 query fragments stay in
+//    registers, K fragments come from ldmatrix (HD / 16 k-steps x 2 token tiles). The query is
+//    rounded unscaled and the scale applied to the fp32 scores, as the prefill kernel does, so a
+//    row gets the same scores whichever of the two kernels runs it. Online softmax in the log2
+//    domain on the accumulator fragments (row statistics over the four lanes of a quad).
 //    O += P V: the score accumulators are repacked as the bf16 A fragment (the FA2 register reuse),
 //    V fragments come from ldmatrix.trans. fp32 accumulation throughout.
 //  * Merge. The warps fold (max, sum, O) into shared memory; after a cluster barrier every CTA merges
@@ -166,10 +168,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int d0 = 16 * ks + 2 * q4, d1 = d0 + 8;
         const float* r0 = qb + (int64_t)g * HD;
         const float* r1 = qb + (int64_t)(g + 8) * HD;
-        qa[ks][0] = v0 ? pack_bf16(r0[d0] * qs, r0[d0 + 1] * qs) : 0u;
-        qa[ks][1] = v1 ? pack_bf16(r1[d0] * qs, r1[d0 + 1] * qs) : 0u;
-        qa[ks][2] = v0 ? pack_bf16(r0[d1] * qs, r0[d1 + 1] * qs) : 0u;
-        qa[ks][3] = v1 ? pack_bf16(r1[d1] * qs, r1[d1 + 1] * qs) : 0u;
+        qa[ks][0] = v0 ? pack_bf16(r0[d0], r0[d0 + 1]) : 0u;
+        qa[ks][1] = v1 ? pack_bf16(r1[d0], r1[d0 + 1]) : 0u;
+        qa[ks][2] = v0 ? pack_bf16(r0[d1], r0[d1 + 1]) : 0u;
+        qa[ks][3] = v1 ? pack_bf16(r1[d1], r1[d1 + 1]) : 0u;
       }
     }
     const uint32_t ring_s = sm100::smem_u32(ring);
@@ -194,13 +196,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma16816(sc[j], qa[2 * pq + 1], kr[2], kr[3]);
         }
       }
-      // mask tokens past the context, online softmax (log2 domain) per head row
+      // scale into the log2 domain, mask tokens past the context, online softmax per head row
       const int tok0 = (b0 + i) * bs + 16 * t + 2 * q4;
 #pragma unroll
       for (int j = 0; j < 2; ++j)
 #pragma unroll
         for (int e = 0; e < 4; ++e)
-          if (tok0 + 8 * j + (e & 1) >= ctx) sc[j][e] = -INFINITY;
+          sc[j][e] = tok0 + 8 * j + (e & 1) < ctx ? sc[j][e] * qs : -INFINITY;
       float mx[2] = {fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1])),
                      fmaxf(fmaxf(sc[0][2], sc[0][3]), fmaxf(sc[1][2], sc[1][3]))};
       float alpha[2], mref[2];
