@@ -52,7 +52,7 @@ void mg_gemv(int64_t fmt, int64_t xin, int64_t epi, const Tensor& tiles, int64_t
              int64_t hfrag_cstride, const optional<Tensor>& hb, const optional<Tensor>& argmax_slots,
              int64_t argmax_offset, const optional<Tensor>& push_recv, const optional<Tensor>& push_epoch,
              const Tensor& part, const Tensor& counters, const Tensor& status, bool pdl, int64_t math,
-             const optional<Tensor>& xinfo) {
+             const optional<Tensor>& xinfo, const std::vector<int64_t>& rope_order) {
   TORCH_CHECK(tiles.is_cuda() && tiles.is_contiguous(), "mg_gemv: tiles must be a contiguous CUDA tensor");
   TORCH_CHECK(tiles.numel() == G * KT * hk::mg_tile_bytes((int)fmt) && KT * 256 == K, "mg_gemv: tile shape mismatch");
   TORCH_CHECK(nb >= 1 && nb <= 8, "mg_gemv: batch columns must be 1..8");
@@ -136,6 +136,15 @@ void mg_gemv(int64_t fmt, int64_t xin, int64_t epi, const Tensor& tiles, int64_t
     a.push_epoch = push_epoch->data_ptr<int>();
     a.push_n = (int)push_recv->numel();
   }
+  if (!rope_order.empty()) {  // (heads, hd, rot, style): tiles packed in RoPE-pair order
+    TORCH_CHECK(rope_order.size() == 4 && epi == hk::MG_STORE, "mg_gemv: rope_order is (heads, hd, rot, style), STORE only");
+    TORCH_CHECK(rope_order[1] % 16 == 0 && rope_order[2] % 16 == 0 && rope_order[2] <= rope_order[1],
+                "mg_gemv: rope_order needs hd and rot multiples of 16");
+    a.rp_heads = (int)rope_order[0];
+    a.rp_hd = (int)rope_order[1];
+    a.rp_rot = (int)rope_order[2];
+    a.rp_style = (int)rope_order[3];
+  }
   a.part = reinterpret_cast<float4*>(part.data_ptr<float>());
   a.counters = counters.data_ptr<int>();
   a.status = status.data_ptr<int>();
@@ -173,6 +182,6 @@ void register_mg_kernels(py::module_& m) {
         py::arg("hfrag_cstride") = 0, py::arg("hb") = py::none(), py::arg("argmax_slots") = py::none(),
         py::arg("argmax_offset") = 0, py::arg("push_recv") = py::none(), py::arg("push_epoch") = py::none(),
         py::arg("part"), py::arg("counters"), py::arg("status"), py::arg("pdl") = false, py::arg("math") = 0,
-        py::arg("xinfo") = py::none());
+        py::arg("xinfo") = py::none(), py::arg("rope_order") = std::vector<int64_t>{});
 }
 }  // namespace hk

@@ -359,4 +359,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   hk::register_tp_kernels(m);
   hk::register_model_kernels(m);
   hk::register_mg_kernels(m);
+  hk::register_ds_kernels(m);
 }

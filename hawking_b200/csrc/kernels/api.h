@@ -149,6 +149,8 @@ struct MgArgs {
   unsigned long long* const* push_recv;  // PUSH: as GemvArgs
   const int* push_epoch;
   int push_n;
+  // QKV packed in RoPE-pair order (rp_heads > 0): the store epilogue writes logical rows
+  int rp_heads, rp_hd, rp_rot, rp_style;
   // scratch: partial fragments [SMs * 3 CTAs * 8 warps][2][32] float4, zeroed counters [G]
   float4* part;
   int* counters;
@@ -164,6 +166,66 @@ void mg_pack_launch(int fmt, int math, const WPlanes& w, const int* rowmap, int 
 void mg_quant_launch(const __nv_bfloat16* x, int64_t x_stride, int nb, int K, uint4* xfrag, int64_t cstride,
                      float2* xinfo, cudaStream_t s, bool pdl);
 void mg_gemv_launch(int fmt, int xin, int epi, const MgArgs& a, int sms, cudaStream_t s, bool pdl);
+
+// ---- persistent decode step (decode_step.cu) ----
+// One launch runs every layer of a dense Llama-family model for up to kDsMaxRows batch rows, plus
+// the final norm and the LM head: QKV GEMV with RoPE and the paged K/V append in its epilogue,
+// split-KV attention on the tensor cores, O GEMV + residual, gate/up GEMV + SwiGLU, down GEMV +
+// residual, all on the W4A16 integer-math tiles of mma_gemv.cu (Q4_K), separated by grid-wide
+// barriers (one CTA per SM, all resident). Weights of the next phase stream into each warp's ring
+// before the barrier that precedes it.
+constexpr int kDsMaxRows = 4;
+struct DsLayer {  // one per layer, in device memory
+  const uint8_t* qkv;   // packed with RoPE pairs as tile rows r / r + 8 (mg pack, rope order)
+  const uint8_t* o;
+  const uint8_t* gu;    // SwiGLU-interleaved gate / up
+  const uint8_t* down;
+  const float* attn_norm;
+  const float* ffn_norm;
+  const float* qkv_bias;  // logical row order; may be null
+};
+struct DsArgs {
+  const DsLayer* layers;
+  int L;
+  int H, F, nh, nkv, hd, rot, rope_style, block_size, max_blocks, num_cache_blocks;
+  int nb;          // batch rows (<= kDsMaxRows)
+  int splits;      // KV splits per (row, kv head)
+  float eps, scale;
+  const int* positions;
+  const int* row_seq;
+  const int* row_ctx;
+  const int* block_tables;
+  const float* rope;  // [max_pos, rot / 2, 2] (cos, sin)
+  float* x;           // [nb, H] residual stream (in: embeddings; out: final hidden state)
+  float* q;           // [nb, nh, hd] roped queries
+  __nv_bfloat16* k_cache;  // [L, blocks, nkv, block_size, hd]
+  __nv_bfloat16* v_cache;
+  float* att_o;       // [nb * nkv * splits, G * hd] split partials
+  float2* att_ml;     // [nb * nkv * splits, G] (max, sum)
+  int* att_cnt;       // [nb * nkv] zeroed
+  uint4* a_limbs;     // attention output, two-limb fragment order: [nb, H / 8] uint4
+  float2* a_info;     // [nb, H / 32]
+  float* hf;          // [nb, F] SwiGLU output
+  uint4* h_limbs;     // [nb, F / 8]
+  float2* h_info;     // [nb, F / 32]
+  int* h_cnt;         // [F / 32] zeroed
+  float4* part;       // split-K partials [grid * 16 warps][2][32]
+  int* counters;      // [max row groups] zeroed
+  const uint8_t* head;  // LM head tiles (plain row order)
+  const float* out_norm;
+  int V;
+  float* logits;      // [nb, V] (may be null)
+  unsigned long long* argmax_slots;  // [nb, kArgmaxSlots] (may be null)
+  unsigned int* bar;  // [2] zeroed: arrivals, generation
+  int* status;
+  long long wait_ns;  // bound of every grid-barrier wait
+};
+// Whether the shape is supported (head_dim 64 / 128, GQA group <= 16, block size 16 / 32 / 64,
+// rot_dim % 16 == 0, H and F multiples of 256, rows <= kDsMaxRows, staging fits shared memory).
+bool ds_supported(const DsArgs& a);
+// CTAs of the persistent grid (one per SM).
+int ds_grid(int device);
+void ds_launch(const DsArgs& a, cudaStream_t s);
 
 // ---- decode ops (decode_ops.cu, attention.cu) ----
 

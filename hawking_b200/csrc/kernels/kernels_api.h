@@ -7,4 +7,5 @@ void register_more_kernels(pybind11::module_& m);
 void register_tp_kernels(pybind11::module_& m);
 void register_model_kernels(pybind11::module_& m);
 void register_mg_kernels(pybind11::module_& m);
+void register_ds_kernels(pybind11::module_& m);
 }  // namespace hk

@@ -204,5 +204,38 @@ __device__ __forceinline__ int pieces_of_group(uint32_t g, uint32_t KT, uint32_t
   return n;
 }
 
+// Head dims of packed tile rows r (0..7) and r + 8 of 16-row group j of a q / k head. The QKV
+// matrix is packed so that the two members of every RoPE pair share a lane: adjacent pairs
+// (2i, 2i + 1) for style 0, halves (i, i + rot/2) for style 1; dims past rot_dim keep their order.
+// p: the pair's frequency index (-1: not rotated).
+__device__ __forceinline__ void rope_pair(int j, int r, int rot, int style, int& da, int& db, int& p) {
+  if (16 * j < rot) {
+    if (style == 0) {
+      da = 16 * j + 2 * r;
+      db = da + 1;
+      p = da >> 1;
+    } else {
+      da = 8 * j + r;
+      db = da + rot / 2;
+      p = da;
+    }
+    return;
+  }
+  da = 16 * j + r;
+  db = da + 8;
+  p = -1;
+}
+
+// Logical row of packed row R of a QKV matrix packed in RoPE-pair order (`heads` q and k heads
+// of hd rows each come first; later rows keep their order).
+__device__ __forceinline__ int64_t rope_unpermute(int64_t R, int hd, int rot, int style, int heads) {
+  const int64_t head = R / hd;
+  if (head >= heads) return R;
+  const int w = (int)(R - head * hd), j = w >> 4, rr = w & 15;
+  int da, db, p;
+  rope_pair(j, rr & 7, rot, style, da, db, p);
+  return head * hd + (rr < 8 ? da : db);
+}
+
 }  // namespace mg
 }  // namespace hk

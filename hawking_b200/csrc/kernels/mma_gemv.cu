@@ -269,9 +269,10 @@ __device__ __forceinline__ void epilogue(const MgArgs& a, uint32_t g_, const flo
   } else {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const int64_t row = g * 16 + (i >> 1) * 8 + r0;
+      int64_t row = g * 16 + (i >> 1) * 8 + r0;
       const int col = 2 * q + (i & 1);
       if (row >= a.N || col >= a.nb) continue;
+      if (EPI == MG_STORE && a.rp_heads) row = rope_unpermute(row, a.rp_hd, a.rp_rot, a.rp_style, a.rp_heads);
       float val = v[i];
       if (a.bias) val += a.bias[row];
       if constexpr (EPI == MG_PUSH) {

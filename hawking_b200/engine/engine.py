@@ -399,6 +399,8 @@ class Engine:
             t.zero_()
         from ..ops import mg
         mg.MgScratch.get(self.model.dev).reset()
+        if getattr(self.model, "dstep", None) is not None:
+            self.model.dstep.reset()
 
     def _sample(self, rows_here, greedy: bool) -> List[int]:
         m = self.model

@@ -74,12 +74,15 @@ class LlamaWeights:
     rope_freqs: Optional[torch.Tensor] = None
     mg_head: Optional[object] = None
 
-    def prepare_mg(self, math: str = "int"):
+    def prepare_mg(self, math: str = "int", rope: Optional[tuple] = None):
         """Re-lay every supported projection for the W4A16 small-batch GEMV (once; the planar
-        GGUF copy stays for the tensor-core GEMM of prefill and large batches)."""
+        GGUF copy stays for the tensor-core GEMM of prefill and large batches). ``rope`` =
+        (q+k heads, head_dim, rot_dim, style) packs QKV in RoPE-pair order (the decode-step kernel
+        rotates in its epilogue; the stand-alone GEMV writes logical rows)."""
         for l in self.layers:
             if l.mg_qkv is None and len(l.wqkv) == 1 and mg.supported(l.wqkv[0]):
-                l.mg_qkv = mg.pack(l.wqkv[0], math=math)
+                order = rope if rope is not None and l.wqkv[0].N % 16 == 0 else None
+                l.mg_qkv = mg.pack(l.wqkv[0], math=math, rope=order)
             if l.mg_o is None and mg.supported(l.wo):
                 l.mg_o = mg.pack(l.wo, math=math)
             if l.moe is None and l.mg_gu is None and l.w_gu is not None and mg.supported(l.w_gu) \
@@ -305,10 +308,16 @@ class LlamaModel:
         self.mg_math = os.environ.get("HK_MG_MATH", "int")
         self.hfrag = None
         if self.small_batch == "w4a16":
-            weights.prepare_mg(self.mg_math)
+            hd_ok = hd % 16 == 0 and cfg.rope_dim % 16 == 0 and cfg.rope_dim <= hd
+            weights.prepare_mg(self.mg_math, rope=(nh + nkv, hd, cfg.rope_dim, cfg.rope_style) if hd_ok else None)
             if any(lw.mg_gu is not None for lw in weights.layers):
                 Fm = max(lw.w_down.K for lw in weights.layers if lw.mg_gu is not None)
                 self.hfrag = mg.FragAct(Fm, self.dev) if self.mg_math == "bf16" else mg.IntFragAct(Fm, self.dev)
+        # bs <= 4 decode as one persistent launch (HK_DSTEP=0 keeps the per-kernel path)
+        self.dstep = None
+        if os.environ.get("HK_DSTEP", "1") == "1" and self.small_batch == "w4a16":
+            from ..ops.dstep import DecodeStep
+            self.dstep = DecodeStep.build(self)
 
     def num_splits(self, rows: int) -> int:
         """KV splits per (row, kv head): the smallest power of two (at most 8, the portable
@@ -357,6 +366,18 @@ class LlamaModel:
         if tp is not None and not tc:
             ops.tp_begin(tp)  # one epoch per forward that uses the push all-reduce sites
         ops.embed(w.embed, inp.ids[:rows], x)
+        if self.dstep is not None and tp is None and not tc and n_logits == 0 and not self.long_runs \
+                and self.small_batch == "w4a16" and self.dstep.supports(rows):
+            # every layer and the LM head in one persistent launch (ops/dstep.py)
+            self.dstep.run(rows, argmax=sample == "greedy")
+            if sample == "greedy":
+                ops.argmax_finalize(self.argmax_slots, rows, self.next_ids)
+            elif sample == "sample":
+                ops.sample(self.logits[:rows], self.temperature[:rows], self.top_k[:rows], self.top_p[:rows],
+                           self.rep_penalty[:rows], None, self.uniforms[:rows], self.next_ids[:rows])
+            if advance:
+                ops.advance(inp.ids, self.next_ids, inp.positions, inp.row_ctx, rows)
+            return
         splits = self.num_splits(rows)
         for l, lw in enumerate(w.layers):
             if tp is not None and not tc:

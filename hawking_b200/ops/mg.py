@@ -44,6 +44,7 @@ class MgWeight:
     KT: int         # 256-column tiles per row group
     swiglu: bool = False
     math: str = "int"
+    rope: Optional[tuple] = None  # (q+k heads, head_dim, rot_dim, style): rows packed in RoPE-pair order
 
     @property
     def nbytes(self) -> int:
@@ -54,10 +55,36 @@ def supported(w: Optional[QWeight]) -> bool:
     return w is not None and w.fmt in MG_FORMATS and w.K % 256 == 0
 
 
-def pack(w: QWeight, swiglu: Optional[int] = None, math: str = "int") -> MgWeight:
+def rope_pair_rows(heads: int, hd: int, rot: int, style: int, n_rows: int) -> torch.Tensor:
+    """Source row of every packed row when a QKV matrix is packed in RoPE-pair order: within each
+    of the first ``heads`` heads (q then k), tile rows r and r + 8 of every 16-row group are the two
+    members of a rotation pair (adjacent dims 2i, 2i+1 for style 0; i, i + rot/2 for style 1), dims
+    past ``rot`` keep their order; later rows (v) are unchanged. The GEMV epilogues map back."""
+    if hd % 16 or rot % 16 or rot > hd:
+        raise ValueError("rope_pair_rows: head_dim and rot_dim must be multiples of 16, rot <= head_dim")
+    w = torch.arange(hd)
+    j, rr = w // 16, w % 16
+    r = rr % 8
+    rotated = 16 * j < rot
+    if style == 0:
+        da, db = 16 * j + 2 * r, 16 * j + 2 * r + 1
+    else:
+        da, db = 8 * j + r, 8 * j + r + rot // 2
+    da = torch.where(rotated, da, 16 * j + r)
+    db = torch.where(rotated, db, 16 * j + r + 8)
+    dim = torch.where(rr < 8, da, db)
+    rows = torch.arange(n_rows)
+    head = rows // hd
+    perm = head * hd + dim[rows % hd]
+    return torch.where(head < heads, perm, rows)
+
+
+def pack(w: QWeight, swiglu: Optional[int] = None, math: str = "int", rope: Optional[tuple] = None) -> MgWeight:
     """Re-lay ``w`` (Q4_K) into fragment-ordered tiles for ``math`` ("int" or "bf16").
     ``swiglu=F``: w is [gate (F rows) | up (F rows)] and tile g holds gate rows 8g..8g+7 followed by
-    the matching up rows."""
+    the matching up rows. ``rope=(q+k heads, hd, rot, style)``: a QKV matrix in RoPE-pair row order
+    (``rope_pair_rows``; the store epilogue writes logical rows, the decode-step kernel rotates
+    each pair in registers)."""
     if math not in MATHS:
         raise ValueError(f"mg.pack: math must be one of {sorted(MATHS)}")
     if not supported(w):
@@ -76,12 +103,17 @@ def pack(w: QWeight, swiglu: Optional[int] = None, math: str = "int") -> MgWeigh
     else:
         G = (w.N + 15) // 16
         r = torch.arange(G * 16, dtype=torch.int64)
-        rowmap = torch.where(r < w.N, r, torch.full_like(r, -1))
+        src = r
+        if rope is not None:
+            if w.N % 16:
+                raise ValueError("mg.pack: a RoPE-ordered QKV matrix needs a multiple of 16 rows")
+            src = rope_pair_rows(*rope, n_rows=G * 16)
+        rowmap = torch.where(r < w.N, src, torch.full_like(r, -1))
         N = w.N
     KT = w.K // 256
     tiles = torch.empty(G * KT * kernels().mg_tile_bytes(int(w.fmt)), dtype=torch.uint8, device=dev)
     kernels().mg_pack(int(w.fmt), w.planes, rowmap.to(torch.int32).to(dev), G, KT, tiles, math=MATHS[math])
-    return MgWeight(tiles, int(w.fmt), N, w.K, G, KT, bool(swiglu), math)
+    return MgWeight(tiles, int(w.fmt), N, w.K, G, KT, bool(swiglu), math, tuple(rope) if rope is not None else None)
 
 
 def frag_index(K: int, nb: int, cstride: int, device) -> torch.Tensor:
@@ -200,4 +232,5 @@ def gemv(mw: MgWeight, nb: int, *, x_norm=None, xb: Optional[torch.Tensor] = Non
         push_recv=push[0] if push is not None else None, push_epoch=push[1] if push is not None else None,
         part=sc.part, counters=sc.counters, status=status if status is not None else sc.status,
         pdl=PDL if pdl is None else pdl, math=MATHS[mw.math],
-        xinfo=xfrag.info if isinstance(xfrag, IntFragAct) else None)
+        xinfo=xfrag.info if isinstance(xfrag, IntFragAct) else None,
+        rope_order=list(mw.rope) if mw.rope is not None else [])

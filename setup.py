@@ -60,7 +60,7 @@ if os.environ.get("HK_SKIP_CUDA", "0") != "1":
             "hawking_b200._kernels",
             sources=_sources("kernels/*.cu", "bindings/kernels_module.cpp", "bindings/kernels_more.cpp",
                              "bindings/kernels_tp.cpp", "bindings/kernels_models.cpp",
-                             "bindings/kernels_mg.cpp"),
+                             "bindings/kernels_mg.cpp", "bindings/kernels_ds.cpp"),
             include_dirs=[os.path.join(ROOT, CSRC, "kernels")],
             extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
             libraries=["cuda"],
