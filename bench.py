@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--profile-step", action="store_true",
                     help="run one eager decode step between cudaProfilerStart/Stop (for ncu --profile-from-start off) "
                          "and exit without a result line")
+    ap.add_argument("--one-launch", type=int, default=1,
+                    help="also time the opt-in persistent decode step (one launch per step), own key")
     ap.add_argument("--w4a8", type=int, default=1,
                     help="also time bs1 decode with the opt-in int8-activation GEMV (reported under its own key)")
     ap.add_argument("--repeats", type=int, default=3,
@@ -621,6 +623,26 @@ def main():
             kv.drop(s)
         m.release_graphs()
         m.small_batch = "w4a16"
+    result_one_launch = None
+    if args.one_launch and getattr(m, "dstep", None) is None and m.tp is None and B <= 4:
+        # the opt-in persistent decode step (every layer + LM head in one launch), same workload,
+        # reported under its own key
+        from hawking_b200.ops.dstep import DecodeStep
+        ds = DecodeStep.build(m)
+        if ds is None:
+            result_one_launch = {"unavailable": "model or shapes outside the persistent decode step"}
+        else:
+            m.release_graphs()
+            m.dstep = ds
+            seqs = setup_decode(B, 4_000_000)
+            msd, clocksd, _ = timed_decode(B)
+            result_one_launch = {"tok_s": round(B * 1000.0 / msd, 2), "ms_per_step": round(msd, 4),
+                                 "clocks": clocksd, "launches_per_step": m.launches_per_graph,
+                                 "note": "opt-in (HK_DSTEP=1): slower than the default per-kernel path so far"}
+            for s_ in seqs:
+                kv.drop(s_)
+            m.release_graphs()
+            m.dstep = None
     result_bs64 = None
     if args.bs64 and B != 64 and m.row_limit < 64:
         # tensor parallel without the tensor-core path (MoE layers): the push all-reduce sites
@@ -705,6 +727,7 @@ def main():
         "bs64": result_bs64,
         "repeat_blocks_ms_per_step": [round(v, 4) for v in rep1],
         "w4a8_opt_in": result_w4a8,
+        "one_launch_step": result_one_launch,
         "ttft_p50_ms": round(ttft_p50, 2),
         "ttft_runs_ms": [round(t, 2) for t in ttfts],
         "weights_gb": round(w.nbytes / 1e9, 3),

@@ -69,7 +69,8 @@ void ds_step(const Tensor& table, const std::vector<int64_t>& dims, double eps, 
              const Tensor& att_ml, const Tensor& att_cnt, const Tensor& a_limbs, const Tensor& a_info,
              const Tensor& hf, const Tensor& h_limbs, const Tensor& h_info, const Tensor& h_cnt, const Tensor& part,
              const Tensor& counters, const Tensor& head, const Tensor& out_norm, const optional<Tensor>& logits,
-             const optional<Tensor>& argmax_slots, const Tensor& bar, const Tensor& status, int64_t wait_ns) {
+             const optional<Tensor>& argmax_slots, const Tensor& bar, const Tensor& status, int64_t wait_ns,
+             const optional<Tensor>& trace, const optional<Tensor>& tstamp) {
   hk::DsArgs a = args_from_dims(dims, eps, scale);
   const int Ka = a.nh * a.hd, G = a.nh / a.nkv, nb = a.nb;
   TORCH_CHECK(table.is_cuda() && table.numel() == (int64_t)(a.L * sizeof(hk::DsLayer)), "ds_step: layer table size");
@@ -120,6 +121,16 @@ void ds_step(const Tensor& table, const std::vector<int64_t>& dims, double eps, 
   a.bar = reinterpret_cast<unsigned int*>(bar.data_ptr<int>());
   a.status = status.data_ptr<int>();
   a.wait_ns = wait_ns > 0 ? wait_ns : 1000000000ll;
+  if (trace.has_value()) {
+    TORCH_CHECK(trace->scalar_type() == at::kInt && trace->is_cuda() && trace->numel() >= hk::ds_grid(x.device().index()) * 4,
+                "ds_step: trace must be int32 [grid, 4]");
+    a.trace = trace->data_ptr<int>();
+  }
+  if (tstamp.has_value()) {
+    TORCH_CHECK(tstamp->scalar_type() == at::kLong && tstamp->is_cuda() && tstamp->numel() >= (5 * a.L + 2) * 4,
+                "ds_step: tstamp must be int64 [5 L + 2, 4]");
+    a.tstamp = reinterpret_cast<long long*>(tstamp->data_ptr<int64_t>());
+  }
   const c10::cuda::CUDAGuard g(x.device());
   hk::ds_launch(a, at::cuda::getCurrentCUDAStream().stream());
 }
@@ -136,6 +147,6 @@ void register_ds_kernels(py::module_& m) {
         py::arg("att_cnt"), py::arg("a_limbs"), py::arg("a_info"), py::arg("hf"), py::arg("h_limbs"),
         py::arg("h_info"), py::arg("h_cnt"), py::arg("part"), py::arg("counters"), py::arg("head"),
         py::arg("out_norm"), py::arg("logits") = py::none(), py::arg("argmax_slots") = py::none(), py::arg("bar"),
-        py::arg("status"), py::arg("wait_ns") = 0);
+        py::arg("status"), py::arg("wait_ns") = 0, py::arg("trace") = py::none(), py::arg("tstamp") = py::none());
 }
 }  // namespace hk

@@ -52,7 +52,8 @@ void mg_gemv(int64_t fmt, int64_t xin, int64_t epi, const Tensor& tiles, int64_t
              int64_t hfrag_cstride, const optional<Tensor>& hb, const optional<Tensor>& argmax_slots,
              int64_t argmax_offset, const optional<Tensor>& push_recv, const optional<Tensor>& push_epoch,
              const Tensor& part, const Tensor& counters, const Tensor& status, bool pdl, int64_t math,
-             const optional<Tensor>& xinfo, const std::vector<int64_t>& rope_order) {
+             const optional<Tensor>& xinfo, const std::vector<int64_t>& rope_order,
+             const std::vector<optional<Tensor>>& rope_epi, const std::vector<int64_t>& rope_dims) {
   TORCH_CHECK(tiles.is_cuda() && tiles.is_contiguous(), "mg_gemv: tiles must be a contiguous CUDA tensor");
   TORCH_CHECK(tiles.numel() == G * KT * hk::mg_tile_bytes((int)fmt) && KT * 256 == K, "mg_gemv: tile shape mismatch");
   TORCH_CHECK(nb >= 1 && nb <= 8, "mg_gemv: batch columns must be 1..8");
@@ -137,13 +138,41 @@ void mg_gemv(int64_t fmt, int64_t xin, int64_t epi, const Tensor& tiles, int64_t
     a.push_n = (int)push_recv->numel();
   }
   if (!rope_order.empty()) {  // (heads, hd, rot, style): tiles packed in RoPE-pair order
-    TORCH_CHECK(rope_order.size() == 4 && epi == hk::MG_STORE, "mg_gemv: rope_order is (heads, hd, rot, style), STORE only");
+    TORCH_CHECK(rope_order.size() == 4 && (epi == hk::MG_STORE || epi == hk::MG_ROPE),
+                "mg_gemv: rope_order is (heads, hd, rot, style), STORE / ROPE epilogues");
     TORCH_CHECK(rope_order[1] % 16 == 0 && rope_order[2] % 16 == 0 && rope_order[2] <= rope_order[1],
                 "mg_gemv: rope_order needs hd and rot multiples of 16");
     a.rp_heads = (int)rope_order[0];
     a.rp_hd = (int)rope_order[1];
     a.rp_rot = (int)rope_order[2];
     a.rp_style = (int)rope_order[3];
+  }
+  if (epi == hk::MG_ROPE) {
+    // rope_epi: (rope table, positions, row_seq, block_tables, k_cache, v_cache, q_out)
+    // rope_dims: (nh, nkv, block_size)
+    TORCH_CHECK(!rope_order.empty() && rope_epi.size() == 7 && rope_dims.size() == 3,
+                "mg_gemv rope: RoPE-ordered tiles, 7 tensors and (nh, nkv, block_size) required");
+    for (int i = 0; i < 7; ++i) TORCH_CHECK(rope_epi[i].has_value() && rope_epi[i]->is_cuda(), "mg_gemv rope: tensor ", i);
+    const Tensor& kc = *rope_epi[4];
+    const Tensor& vc = *rope_epi[5];
+    TORCH_CHECK(kc.scalar_type() == at::kBFloat16 && kc.is_contiguous() && vc.is_contiguous() &&
+                    kc.size(-1) == rope_order[1] && kc.size(-2) == rope_dims[2] && kc.size(-3) == rope_dims[1],
+                "mg_gemv rope: caches must be contiguous bf16 [blocks, nkv, block_size, hd]");
+    TORCH_CHECK(rope_epi[6]->scalar_type() == at::kFloat && rope_epi[6]->numel() >= nb * rope_dims[0] * rope_order[1],
+                "mg_gemv rope: q_out must be fp32 [nb, nh, hd]");
+    TORCH_CHECK(rope_order[0] == rope_dims[0] + rope_dims[1] && N == (rope_dims[0] + 2 * rope_dims[1]) * rope_order[1],
+                "mg_gemv rope: head counts do not match the matrix");
+    a.rope = rope_epi[0]->data_ptr<float>();
+    a.positions = rope_epi[1]->data_ptr<int>();
+    a.row_seq = rope_epi[2]->data_ptr<int>();
+    a.block_tables = rope_epi[3]->data_ptr<int>();
+    a.max_blocks = (int)rope_epi[3]->size(1);
+    a.block_size = (int)rope_dims[2];
+    a.k_cache = ptr<__nv_bfloat16>(kc);
+    a.v_cache = ptr<__nv_bfloat16>(vc);
+    a.q_out = rope_epi[6]->data_ptr<float>();
+    a.nh = (int)rope_dims[0];
+    a.nkv = (int)rope_dims[1];
   }
   a.part = reinterpret_cast<float4*>(part.data_ptr<float>());
   a.counters = counters.data_ptr<int>();
@@ -182,6 +211,7 @@ void register_mg_kernels(py::module_& m) {
         py::arg("hfrag_cstride") = 0, py::arg("hb") = py::none(), py::arg("argmax_slots") = py::none(),
         py::arg("argmax_offset") = 0, py::arg("push_recv") = py::none(), py::arg("push_epoch") = py::none(),
         py::arg("part"), py::arg("counters"), py::arg("status"), py::arg("pdl") = false, py::arg("math") = 0,
-        py::arg("xinfo") = py::none(), py::arg("rope_order") = std::vector<int64_t>{});
+        py::arg("xinfo") = py::none(), py::arg("rope_order") = std::vector<int64_t>{},
+        py::arg("rope_epi") = std::vector<optional<Tensor>>{}, py::arg("rope_dims") = std::vector<int64_t>{});
 }
 }  // namespace hk

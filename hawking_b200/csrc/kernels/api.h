@@ -112,7 +112,7 @@ void gemv_launch(int fmt, int epi, const GemvArgs& a, int nb, cudaStream_t s, bo
 // W4A16: weights in fragment-ordered tiles of 16 rows x 256 columns (mg_pack_launch), bf16
 // activations, fp32 accumulation. See mma_gemv.cu for the design.
 enum MgInput : int { MG_X_NORM = 0, MG_X_BF16 = 1, MG_X_FRAG = 2, MG_X_FRAG_SMEM = 3 };  // 3: internal (FRAG staged)
-enum MgEpilogue : int { MG_STORE = 0, MG_RESID = 1, MG_SWIGLU = 2, MG_PUSH = 3 };
+enum MgEpilogue : int { MG_STORE = 0, MG_RESID = 1, MG_SWIGLU = 2, MG_PUSH = 3, MG_ROPE = 4 };
 // Math of the tiles: MG_MATH_BF16 (bf16 activations, bf16 MMA; tiles packed for it) or MG_MATH_INT
 // (activations as 16-bit fixed point per 32-element block, held as two int8 limbs, u8 x s8 MMA;
 // tiles packed for it). The input modes are the same; MG_X_FRAG of the integer math is the layout
@@ -151,6 +151,16 @@ struct MgArgs {
   int push_n;
   // QKV packed in RoPE-pair order (rp_heads > 0): the store epilogue writes logical rows
   int rp_heads, rp_hd, rp_rot, rp_style;
+  // MG_ROPE epilogue (QKV packed in RoPE-pair order): RoPE + paged K/V append, q to q_out
+  const float* rope;
+  const int* positions;
+  const int* row_seq;
+  const int* block_tables;
+  int max_blocks, block_size;
+  __nv_bfloat16* k_cache;
+  __nv_bfloat16* v_cache;
+  float* q_out;
+  int nh, nkv;
   // scratch: partial fragments [SMs * 3 CTAs * 8 warps][2][32] float4, zeroed counters [G]
   float4* part;
   int* counters;
@@ -219,6 +229,14 @@ struct DsArgs {
   unsigned int* bar;  // [2] zeroed: arrivals, generation
   int* status;
   long long wait_ns;  // bound of every grid-barrier wait
+  // optional [grid][4]: barriers passed, and the first failed wait of the CTA (site: 1 weight
+  // ring, 2 attention K/V unit, 3 attention ring slot, 4 activation copy, 5 grid barrier; phase
+  // 5l + k; warp)
+  int* trace;
+  // optional [5 * L + 2][4] globaltimer (ns): row 0 kernel start; row p + 1 for phase p: CTA 0's
+  // exit from the barrier closing it, earliest and latest CTA arrival at that barrier, CTA 0's end
+  // of activation staging (phases with staging); the caller presets columns 1 / 2 to max / 0
+  long long* tstamp;
 };
 // Whether the shape is supported (head_dim 64 / 128, GQA group <= 16, block size 16 / 32 / 64,
 // rot_dim % 16 == 0, H and F multiples of 256, rows <= kDsMaxRows, staging fits shared memory).

@@ -56,12 +56,13 @@ constexpr int kTpc = 2;              // tiles per stage
 constexpr int TB = Tile<WF_Q4_K>::BYTES;
 constexpr int kScaleBytes = 16 * 8 * 8;
 constexpr int kAttnStages = 4;       // KV ring: one 16-token unit (K and V) per stage
-constexpr int kAttnConsumers = 8;    // warps 0..7 compute attention, warp 8 lane 0 issues the loads
+constexpr int kAttnConsumers = 8;    // warps 0..7 compute attention (a pair per stage), warp 8 lane 0 loads
+static_assert(kAttnConsumers == 2 * kAttnStages, "one warp pair per KV ring stage");
 constexpr int kProducerWarp = 8;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr int kRingBytes = kWarps * kStages * kTpc * TB;
-constexpr int kBarOff = kRingBytes + kWarps * kScaleBytes;   // mbarriers, reduction scratch
-constexpr int kXsOff = kBarOff + 1024;                        // activations / attention region
+constexpr int kBarOff = kRingBytes + kWarps * kScaleBytes;   // mbarriers, reduction scratch, cursors
+constexpr int kXsOff = kBarOff + 2048;                        // activations / attention region
 constexpr int kSmemMax = 232448;                              // 227 KB per CTA
 constexpr int kXsBytes = kSmemMax - kXsOff - 1024;            // (1024 of alignment slack)
 static_assert(kXsOff % 1024 == 0, "attention stages need 1024-byte alignment");
@@ -84,14 +85,35 @@ __device__ __forceinline__ long long gtimer() {
 // Generic-proxy global writes (the K/V append) before async-proxy reads (TMA) in a later phase.
 __device__ __forceinline__ void fence_proxy_async_all() { asm volatile("fence.proxy.async;" ::: "memory"); }
 
+// First failed wait of this CTA (site, phase, warp) into the optional trace.
+__device__ __forceinline__ void trace_fail(const DsArgs& a, int site, int phase) {
+  if (!a.trace) return;
+  int* t = a.trace + blockIdx.x * 4;
+  if (atomicCAS(t + 1, 0, site) == 0) {
+    t[2] = phase;
+    t[3] = threadIdx.x >> 5;
+  }
+}
+
 // Grid-wide barrier of `n` CTAs: arrival counter bar[0], generation bar[1]. The last arrival resets
 // the counter and publishes the next generation (release); the others poll it (acquire) for at
 // most wait_ns, and leave early once the status word is set. Returns false on failure.
-__device__ bool grid_sync(unsigned* bar, unsigned n, int* status, long long wait_ns, int* s_flag) {
-  fence_proxy_async_all();
+// `proxy`: the phase before wrote memory (global K/V, or shared memory) that the async proxy (TMA,
+// bulk copies) reads after the barrier; every thread fences its own generic writes.
+__device__ __forceinline__ bool grid_sync(const DsArgs& a, int phase, int* s_flag, bool proxy) {
+  unsigned* bar = a.bar;
+  const unsigned n = gridDim.x;
+  int* status = a.status;
+  const long long wait_ns = a.wait_ns;
+  if (proxy) fence_proxy_async_all();
   __syncthreads();
   if (threadIdx.x == 0) {
     int ok = 1;
+    if (a.tstamp) {  // earliest and latest arrival over the CTAs
+      const unsigned long long t = (unsigned long long)gtimer();
+      atomicMin(reinterpret_cast<unsigned long long*>(a.tstamp) + (phase + 1) * 4 + 1, t);
+      atomicMax(reinterpret_cast<unsigned long long*>(a.tstamp) + (phase + 1) * 4 + 2, t);
+    }
     const unsigned gen = ld_acquire(bar + 1);
     __threadfence();
     if (atomicAdd(bar, 1u) == n - 1) {
@@ -106,6 +128,7 @@ __device__ bool grid_sync(unsigned* bar, unsigned n, int* status, long long wait
           if (*((volatile int*)status) != 0) { ok = 0; break; }
           if (gtimer() - t0 > wait_ns) {
             set_error(status, HK_ERR_PEER_TIMEOUT);
+            trace_fail(a, 5, phase);
             ok = 0;
             break;
           }
@@ -113,11 +136,13 @@ __device__ bool grid_sync(unsigned* bar, unsigned n, int* status, long long wait
       }
     }
     if (ok && *((volatile int*)status) != 0) ok = 0;
+    if (ok && a.trace) a.trace[blockIdx.x * 4] += 1;
+    if (ok && a.tstamp && blockIdx.x == 0) a.tstamp[(phase + 1) * 4] = gtimer();
     *s_flag = ok;
   }
   __syncthreads();
   const bool ok = *(volatile int*)s_flag != 0;
-  fence_proxy_async_all();
+  if (proxy && threadIdx.x == 0) fence_proxy_async_all();
   return ok;
 }
 
@@ -167,8 +192,9 @@ __device__ void stage_norm(const float* x, int H, int nb, const float* w, float 
 // Limbs + info already in global memory (written earlier in this launch) -> shared memory, one
 // bulk copy per column and one for its info, on `bar` (single use per phase: parity tracked by the
 // caller).
-__device__ bool stage_copy(const uint4* limbs, const float2* ginfo, int K, int nb, uint4* xs, int64_t cs,
-                           float2* info, int64_t is, uint64_t* bar, uint32_t parity, int* status) {
+__device__ bool stage_copy(const DsArgs& a, int phase, const uint4* limbs, const float2* ginfo, int K, int nb,
+                           uint4* xs, int64_t cs, float2* info, int64_t is, uint64_t* bar, uint32_t parity) {
+  int* status = a.status;
   if (threadIdx.x == 0) {
     const uint32_t colb = (uint32_t)K * 2, infb = (uint32_t)(K / 32) * 8;
     sm100::mbar_arrive_expect_tx(bar, (colb + infb) * (uint32_t)nb);
@@ -180,7 +206,10 @@ __device__ bool stage_copy(const uint4* limbs, const float2* ginfo, int K, int n
   const bool ok = sm100::mbar_wait(bar, parity, status);
   // a wait that left early (status set elsewhere) still lets the copies land before the region
   // is reused or the CTA exits
-  if (!ok && threadIdx.x == 0) sm100::mbar_wait(bar, parity, nullptr, 1u << 22);
+  if (!ok && threadIdx.x == 0) {
+    trace_fail(a, 4, phase);
+    sm100::mbar_wait(bar, parity, nullptr, 1u << 22);
+  }
   return ok;
 }
 
@@ -217,44 +246,10 @@ __device__ __forceinline__ void epilogue(const DsArgs& a, const EpiCtx& e, uint3
                                          int lane) {
   const int r0 = lane >> 2, q = lane & 3;
   if constexpr (EPI == EPI_QKV) {
-    const int R = (int)g * 16, head = R / a.hd, j = (R % a.hd) / 16;
-    const int kind = head < a.nh ? 0 : (head < a.nh + a.nkv ? 1 : 2);
-    int da, db, p = -1;
-    if (kind < 2) {
-      rope_pair(j, r0, a.rot, a.rope_style, da, db, p);
-    } else {
-      da = 16 * j + r0;
-      db = da + 8;
-    }
-#pragma unroll
-    for (int i = 0; i < (NB > 1 ? 2 : 1); ++i) {
-      const int col = 2 * q + i;
-      if (col >= a.nb) continue;
-      float x0 = v[i], x1 = v[2 + i];
-      if (e.qkv_bias) {
-        x0 += e.qkv_bias[head * a.hd + da];
-        x1 += e.qkv_bias[head * a.hd + db];
-      }
-      const int pos = a.positions[col];
-      if (p >= 0) {
-        const float2 cs = *reinterpret_cast<const float2*>(a.rope + ((int64_t)pos * (a.rot / 2) + p) * 2);
-        const float ya = x0 * cs.x - x1 * cs.y, yb = x0 * cs.y + x1 * cs.x;
-        x0 = ya;
-        x1 = yb;
-      }
-      if (kind == 0) {
-        float* dst = a.q + ((int64_t)col * a.nh + head) * a.hd;
-        __stcg(dst + da, x0);
-        __stcg(dst + db, x1);
-      } else {
-        const int kh = head - a.nh - (kind == 2 ? a.nkv : 0);
-        const int blk = a.block_tables[(int64_t)a.row_seq[col] * a.max_blocks + pos / a.block_size];
-        const int64_t row = (((int64_t)e.l * a.num_cache_blocks + blk) * a.nkv + kh) * a.block_size + pos % a.block_size;
-        __nv_bfloat16* dst = (kind == 1 ? a.k_cache : a.v_cache) + row * a.hd;
-        dst[da] = __float2bfloat16_rn(x0);
-        dst[db] = __float2bfloat16_rn(x1);
-      }
-    }
+    const int64_t layer = (int64_t)e.l * a.num_cache_blocks * a.nkv * a.block_size * a.hd;
+    const RopeEpi r{a.rope, a.positions, a.row_seq, a.block_tables, a.max_blocks, a.block_size,
+                    a.k_cache + layer, a.v_cache + layer, a.q, e.qkv_bias, a.nh, a.nkv, a.hd, a.rot, a.rope_style};
+    rope_epilogue<NB>(r, a.nb, g, v, lane);
   } else if constexpr (EPI == EPI_RESID) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -319,57 +314,64 @@ __device__ __forceinline__ Mat matrix_of(const DsArgs& a, int ph) {
 }
 __device__ __forceinline__ int next_weight_phase(int ph) { return ph % 5 == PH_QKV ? ph + 2 : ph + 1; }
 
+// Issue cursor of a warp's stream: lane 0 only, in shared memory (keeps the registers of the
+// consuming loop free).
+struct IssueCursor {
+  const uint8_t* itiles;
+  uint32_t issued, ichunk, inchunks, it0, intiles;
+  int iph;
+};
+static_assert(sizeof(IssueCursor) <= 64, "one 64-byte slot per warp");
+
 struct WarpStream {
   uint8_t* ring;
   uint64_t* bars;
-  uint32_t issued, cons;  // chunks issued / consumed so far (one sequence over all phases)
-  int iph;                // phase of the issue cursor
-  uint32_t ichunk, inchunks, it0, intiles;
-  const uint8_t* itiles;
+  IssueCursor* ic;
+  uint32_t cons;  // chunks consumed so far (one sequence over all phases; every lane)
 
-  __device__ void open(const DsArgs& a, int ph, uint32_t p, uint32_t P) {
-    iph = ph;
-    ichunk = 0;
+  __device__ static void open(const DsArgs& a, IssueCursor& c, int ph, uint32_t p, uint32_t P) {
+    c.iph = ph;
+    c.ichunk = 0;
     if (ph > 5 * a.L) {
-      inchunks = 0;
+      c.inchunks = 0;
       return;
     }
     const Mat m = matrix_of(a, ph);
     const uint32_t T = m.G * m.KT;
-    it0 = start_of(p, T, P);
-    intiles = start_of(p + 1, T, P) - it0;
-    inchunks = (intiles + kTpc - 1) / kTpc;
-    itiles = m.tiles;
+    c.it0 = start_of(p, T, P);
+    c.intiles = start_of(p + 1, T, P) - c.it0;
+    c.inchunks = (c.intiles + kTpc - 1) / kTpc;
+    c.itiles = m.tiles;
   }
-  // Issue the next chunk of the sequence (lane 0 copies; every lane keeps the cursor).
+  // Lane 0: issue the next chunk of the sequence, whichever phase it belongs to.
   __device__ void issue_next(const DsArgs& a, uint32_t p, uint32_t P, int lane) {
-    while (ichunk >= inchunks) {
-      if (iph >= 5 * a.L) return;
-      open(a, next_weight_phase(iph), p, P);
+    if (lane != 0) return;
+    IssueCursor& c = *ic;
+    while (c.ichunk >= c.inchunks) {
+      if (c.iph >= 5 * a.L) return;
+      open(a, c, next_weight_phase(c.iph), p, P);
     }
-    const uint32_t st = issued % kStages;
-    const uint32_t cnt = min((uint32_t)kTpc, intiles - ichunk * kTpc);
-    if (lane == 0) {
-      sm100::mbar_arrive_expect_tx(&bars[st], cnt * TB);
-      sm100::bulk_g2s(ring + st * kTpc * TB, itiles + (int64_t)(it0 + ichunk * kTpc) * TB, cnt * TB, &bars[st]);
-    }
-    ++ichunk;
-    ++issued;
+    const uint32_t st = c.issued % kStages;
+    const uint32_t cnt = min((uint32_t)kTpc, c.intiles - c.ichunk * kTpc);
+    sm100::mbar_arrive_expect_tx(&bars[st], cnt * TB);
+    sm100::bulk_g2s(ring + st * kTpc * TB, c.itiles + (int64_t)(c.it0 + c.ichunk * kTpc) * TB, cnt * TB, &bars[st]);
+    ++c.ichunk;
+    ++c.issued;
   }
   // Wait (bounded, no early exit) for every chunk still in flight: before the CTA may exit.
   __device__ void drain(int lane) {
     if (lane == 0)
-      for (uint32_t k = cons; k < issued; ++k)
+      for (uint32_t k = cons; k < ic->issued; ++k)
         sm100::mbar_wait(&bars[k % kStages], (k / kStages) & 1, nullptr, 1u << 22);
-    cons = issued;
   }
 };
 
 // One GEMV phase for this warp: consume its tile range of matrix `m` (the chunks at the head of its
 // stream), with the deterministic split-K fix-up of mma_gemv.cu, then the epilogue.
 template <int NB, int EPI>
-__device__ bool gemv_phase(const DsArgs& a, const EpiCtx& e, const Mat& m, const XInt& xi, WarpStream& ws,
-                           float2* scs, uint32_t p, uint32_t P, int lane) {
+__device__ __forceinline__ bool gemv_phase(const DsArgs& a, const EpiCtx& e, int ph, const XInt& xi, WarpStream& ws, float2* scs,
+                           uint32_t p, uint32_t P, int lane) {
+  const Mat m = matrix_of(a, ph);
   const uint32_t KT = m.KT, T = m.G * KT;
   const uint32_t t0 = start_of(p, T, P), t1 = start_of(p + 1, T, P);
   const int n_tiles = (int)(t1 - t0);
@@ -379,7 +381,10 @@ __device__ bool gemv_phase(const DsArgs& a, const EpiCtx& e, const Mat& m, const
   int u = 0;
   for (int i = 0; i < n_tiles; ++i) {
     const uint32_t st = ws.cons % kStages;
-    if (u == 0 && !sm100::mbar_wait(&ws.bars[st], (ws.cons / kStages) & 1, a.status)) return false;
+    if (u == 0 && !sm100::mbar_wait(&ws.bars[st], (ws.cons / kStages) & 1, a.status)) {
+      if (lane == 0) trace_fail(a, 1, ph);
+      return false;
+    }
     consume_q4k_int<NB>(ws.ring + (st * kTpc + u) * TB, (int)s, xi, a.nb, scs, lane, sum);
     if (++u == kTpc || i == n_tiles - 1) {  // chunk consumed: the next one of the stream takes its stage
       u = 0;
@@ -440,7 +445,7 @@ struct AttnSmem {
 };
 
 template <int HD>
-__device__ bool attn_phase(const DsArgs& a, int l, const CUtensorMap* tk, const CUtensorMap* tv, const AttnSmem& sm,
+__device__ __forceinline__ bool attn_phase(const DsArgs& a, int l, const CUtensorMap* tk, const CUtensorMap* tv, const AttnSmem& sm,
                            uint64_t* afull, uint64_t* aempty, uint32_t& useq) {
   constexpr int NKS = HD / 16, NDT = HD / 8;
   constexpr uint32_t kUnitBytes = 2 * 16 * HD * 2;  // K and V of 16 tokens
@@ -464,15 +469,16 @@ __device__ bool attn_phase(const DsArgs& a, int l, const CUtensorMap* tk, const 
     if (tid < 16) sm.s_l[tid] = 0.f;
     __syncthreads();
     float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
-    float o[NDT][4];
+    float o[NDT / 2][4];  // this warp's half of the head dims
 #pragma unroll
-    for (int d = 0; d < NDT; ++d) o[d][0] = o[d][1] = o[d][2] = o[d][3] = 0.f;
+    for (int d = 0; d < NDT / 2; ++d) o[d][0] = o[d][1] = o[d][2] = o[d][3] = 0.f;
     if (warp == kProducerWarp) {
       if (lane == 0) {
         int issued = 0;
         for (int u = 0; u < n_units && ok; ++u) {
           const uint32_t sq = useq + u, st = sq % kAttnStages;
           if (sq >= kAttnStages && !sm100::mbar_wait(&aempty[st], ((sq / kAttnStages) - 1) & 1, a.status)) {
+            trace_fail(a, 3, 5 * l + PH_ATTN);
             ok = false;
             break;
           }
@@ -513,9 +519,15 @@ __device__ bool attn_phase(const DsArgs& a, int l, const CUtensorMap* tk, const 
         }
       }
       const float qs = a.scale * kLog2e;
-      for (int u = warp; u < n_units && ok; u += kAttnConsumers) {
+      // stage st belongs to the warp pair (st, st + 4): both wait every phase of it in order (a
+      // parity wait is sound only for a waiter that saw the stage's previous phase), both form
+      // the scores, and each takes half of the head dims in P V
+      const int pair = warp & (kAttnStages - 1), half = warp / kAttnStages;
+      const int u0 = (int)((pair + kAttnStages - useq % kAttnStages) % kAttnStages);
+      for (int u = u0; u < n_units && ok; u += kAttnStages) {
         const uint32_t sq = useq + u, st = sq % kAttnStages;
         if (!sm100::mbar_wait(&afull[st], (sq / kAttnStages) & 1, a.status)) {
+          if (lane == 0) trace_fail(a, 2, 5 * l + PH_ATTN);
           ok = false;
           break;
         }
@@ -561,9 +573,9 @@ __device__ bool attn_phase(const DsArgs& a, int l, const CUtensorMap* tk, const 
                                 pack_bf16(pv[1][0], pv[1][1]), pack_bf16(pv[1][2], pv[1][3])};
         const int vrow = ((lane >> 3) & 1) * 8 + (lane & 7);
 #pragma unroll
-        for (int dd = 0; dd < NDT / 2; ++dd) {
+        for (int dd = 0; dd < NDT / 4; ++dd) {
           uint32_t vr[4];
-          ldsm_x4_t(sw_addr(vb, 16, vrow, 2 * dd + (lane >> 4)), vr);
+          ldsm_x4_t(sw_addr(vb, 16, vrow, 2 * (half * (NDT / 4) + dd) + (lane >> 4)), vr);
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             float* od = o[2 * dd + h];
@@ -596,13 +608,15 @@ __device__ bool attn_phase(const DsArgs& a, int l, const CUtensorMap* tk, const 
 #pragma unroll
         for (int w = 0; w < kAttnConsumers; ++w) M = fmaxf(M, sm.s_wm[w * 16 + row]);
         const float f = m_r[h] == -INFINITY ? 0.f : exp2f(m_r[h] - M);
+        const int half = warp / kAttnStages;
         if (f != 0.f && row < G) {
 #pragma unroll
-          for (int d = 0; d < NDT; ++d) {
-            atomicAdd(&sm.s_o[row * HD + 8 * d + 2 * q4], o[d][2 * h] * f);
-            atomicAdd(&sm.s_o[row * HD + 8 * d + 2 * q4 + 1], o[d][2 * h + 1] * f);
+          for (int d = 0; d < NDT / 2; ++d) {
+            const int col = half * (HD / 2) + 8 * d + 2 * q4;
+            atomicAdd(&sm.s_o[row * HD + col], o[d][2 * h] * f);
+            atomicAdd(&sm.s_o[row * HD + col + 1], o[d][2 * h + 1] * f);
           }
-          if (q4 == 0) atomicAdd(&sm.s_l[row], l_r[h] * f);
+          if (q4 == 0 && half == 0) atomicAdd(&sm.s_l[row], l_r[h] * f);  // both halves hold the same sums
         }
         if (warp == 0 && q4 == 0) sm.s_m[row] = M;
       }
@@ -689,21 +703,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < kAttnStages; ++s) {
       sm100::mbar_init(&afull[s], 1);
-      sm100::mbar_init(&aempty[s], 1);
+      sm100::mbar_init(&aempty[s], kAttnConsumers / kAttnStages);  // both warps of the stage's pair
     }
     sm100::mbar_init(xbar, 1);
     sm100::prefetch_tmap(&tk);
     sm100::prefetch_tmap(&tv);
   }
   if (threadIdx.x == 0 || lane == 0) sm100::fence_barrier_init();
+  if (threadIdx.x == 0 && blockIdx.x == 0 && a.tstamp) a.tstamp[0] = gtimer();
+  if (threadIdx.x == 0 && a.tstamp) a.tstamp[2] = 0;  // (slot 2 of row 0 unused)
   __syncthreads();
 
   const uint32_t P = gridDim.x * kWarps, p = blockIdx.x * kWarps + warp;
   WarpStream ws;
   ws.ring = smem + warp * kStages * kTpc * TB;
   ws.bars = wbars + warp * kStages;
-  ws.issued = ws.cons = 0;
-  ws.open(a, 0, p, P);
+  ws.ic = reinterpret_cast<IssueCursor*>(smem + kBarOff + 1024 + warp * 64);
+  ws.cons = 0;
+  if (lane == 0) {
+    ws.ic->issued = 0;
+    WarpStream::open(a, *ws.ic, 0, p, P);
+  }
   for (int k = 0; k < kStages; ++k) ws.issue_next(a, p, P, lane);
 
   const int H = a.H, F = a.F, Ka = a.nh * HD;
@@ -720,48 +740,50 @@ __global__ void __launch_bounds__(kThreads, 1)
   const bool down_smem = (int64_t)a.nb * ((F / 8 + 1) * 16 + (F / 32) * 8) <= kXsBytes;
   uint32_t useq = 0, xph = 0;
   bool ok = true;
-  const unsigned nctas = gridDim.x;
 
   for (int l = 0; l < a.L && ok; ++l) {
     const DsLayer ly = a.layers[l];
     const EpiCtx e{l, ly.qkv_bias};
     // A: RMSNorm -> QKV, RoPE + K/V append
     stage_norm(a.x, H, a.nb, ly.attn_norm, a.eps, xs, csH, info_at(csH), isH, red);
-    gemv_phase<NB, EPI_QKV>(a, e, matrix_of(a, 5 * l + PH_QKV), XInt{xs, csH, info_at(csH), isH}, ws, scs, p, P, lane);
-    if (!(ok = grid_sync(a.bar, nctas, a.status, a.wait_ns, s_flag))) break;
+    if (a.tstamp && blockIdx.x == 0 && threadIdx.x == 0) a.tstamp[(5 * l + PH_QKV + 1) * 4 + 3] = gtimer();
+    gemv_phase<NB, EPI_QKV>(a, e, 5 * l + PH_QKV, XInt{xs, csH, info_at(csH), isH}, ws, scs, p, P, lane);
+    if (!(ok = grid_sync(a, 5 * l + PH_QKV, s_flag, true))) break;
     // B: attention -> limbs of the O projection's input
     attn_phase<HD>(a, l, &tk, &tv, as, afull, aempty, useq);
-    if (!(ok = grid_sync(a.bar, nctas, a.status, a.wait_ns, s_flag))) break;
+    if (!(ok = grid_sync(a, 5 * l + PH_ATTN, s_flag, true))) break;
     // C: O projection + residual
     {
       const int64_t cs = Ka / 8 + 1, is = Ka / 32;
-      stage_copy(a.a_limbs, a.a_info, Ka, a.nb, xs, cs, info_at(cs), is, xbar, xph++ & 1, a.status);
-      gemv_phase<NB, EPI_RESID>(a, e, matrix_of(a, 5 * l + PH_O), XInt{xs, cs, info_at(cs), is}, ws, scs, p, P, lane);
+      stage_copy(a, 5 * l + PH_O, a.a_limbs, a.a_info, Ka, a.nb, xs, cs, info_at(cs), is, xbar, xph++ & 1);
+      gemv_phase<NB, EPI_RESID>(a, e, 5 * l + PH_O, XInt{xs, cs, info_at(cs), is}, ws, scs, p, P, lane);
     }
-    if (!(ok = grid_sync(a.bar, nctas, a.status, a.wait_ns, s_flag))) break;
+    if (!(ok = grid_sync(a, 5 * l + PH_O, s_flag, false))) break;
     // D: RMSNorm -> gate/up, SwiGLU (+ block quantisation of h)
     stage_norm(a.x, H, a.nb, ly.ffn_norm, a.eps, xs, csH, info_at(csH), isH, red);
-    gemv_phase<NB, EPI_SWIGLU>(a, e, matrix_of(a, 5 * l + PH_GU), XInt{xs, csH, info_at(csH), isH}, ws, scs, p, P,
+    if (a.tstamp && blockIdx.x == 0 && threadIdx.x == 0) a.tstamp[(5 * l + PH_GU + 1) * 4 + 3] = gtimer();
+    gemv_phase<NB, EPI_SWIGLU>(a, e, 5 * l + PH_GU, XInt{xs, csH, info_at(csH), isH}, ws, scs, p, P,
                                lane);
-    if (!(ok = grid_sync(a.bar, nctas, a.status, a.wait_ns, s_flag))) break;
+    if (!(ok = grid_sync(a, 5 * l + PH_GU, s_flag, true))) break;
     // E: down projection + residual
     if (down_smem) {
       const int64_t cs = F / 8 + 1, is = F / 32;
-      stage_copy(a.h_limbs, a.h_info, F, a.nb, xs, cs, info_at(cs), is, xbar, xph++ & 1, a.status);
-      gemv_phase<NB, EPI_RESID>(a, e, matrix_of(a, 5 * l + PH_DOWN), XInt{xs, cs, info_at(cs), is}, ws, scs, p, P,
+      stage_copy(a, 5 * l + PH_DOWN, a.h_limbs, a.h_info, F, a.nb, xs, cs, info_at(cs), is, xbar, xph++ & 1);
+      gemv_phase<NB, EPI_RESID>(a, e, 5 * l + PH_DOWN, XInt{xs, cs, info_at(cs), is}, ws, scs, p, P,
                                 lane);
     } else {
-      gemv_phase<NB, EPI_RESID>(a, e, matrix_of(a, 5 * l + PH_DOWN), XInt{a.h_limbs, F / 8, a.h_info, F / 32}, ws,
+      gemv_phase<NB, EPI_RESID>(a, e, 5 * l + PH_DOWN, XInt{a.h_limbs, F / 8, a.h_info, F / 32}, ws,
                                 scs, p, P, lane);
     }
-    if (!(ok = grid_sync(a.bar, nctas, a.status, a.wait_ns, s_flag))) break;
+    if (!(ok = grid_sync(a, 5 * l + PH_DOWN, s_flag, false))) break;
   }
   if (ok) {
     // final RMSNorm -> LM head (logits, greedy keys)
     stage_norm(a.x, H, a.nb, a.out_norm, a.eps, xs, csH, info_at(csH), isH, red);
-    gemv_phase<NB, EPI_HEAD>(a, EpiCtx{a.L, nullptr}, matrix_of(a, 5 * a.L), XInt{xs, csH, info_at(csH), isH}, ws,
+    gemv_phase<NB, EPI_HEAD>(a, EpiCtx{a.L, nullptr}, 5 * a.L, XInt{xs, csH, info_at(csH), isH}, ws,
                              scs, p, P, lane);
   }
+  if (ok && a.tstamp && blockIdx.x == 0 && threadIdx.x == 0) a.tstamp[(5 * a.L + 1) * 4] = gtimer();
   ws.drain(lane);  // nothing in flight on the normal path; after a failure, the prefetched chunks
 }
 

@@ -237,5 +237,64 @@ __device__ __forceinline__ int64_t rope_unpermute(int64_t R, int hd, int rot, in
   return head * hd + (rr < 8 ? da : db);
 }
 
+// QKV epilogue in RoPE-pair order (one row group of 16 packed rows; the lane holds rows r0, r0 + 8
+// x columns 2q, 2q + 1): bias, rotation of q / k pairs in registers, q to fp32 rows, k / v to the
+// paged bf16 cache of one layer at each column's position.
+struct RopeEpi {
+  const float* rope;         // [max_pos, rot / 2, 2] (cos, sin)
+  const int* positions;      // [nb]
+  const int* row_seq;        // [nb]
+  const int* block_tables;   // [seqs, max_blocks]
+  int max_blocks, block_size;
+  __nv_bfloat16* k_cache;    // this layer's [blocks, nkv, block_size, hd]
+  __nv_bfloat16* v_cache;
+  float* q;                  // [nb, nh, hd]
+  const float* bias;         // logical row order; may be null
+  int nh, nkv, hd, rot, style;
+};
+
+template <int NB>
+__device__ __forceinline__ void rope_epilogue(const RopeEpi& r, int nb, uint32_t g, const float (&v)[4], int lane) {
+  const int r0 = lane >> 2, q = lane & 3;
+  const int R = (int)g * 16, head = R / r.hd, j = (R % r.hd) / 16;
+  const int kind = head < r.nh ? 0 : (head < r.nh + r.nkv ? 1 : 2);
+  int da, db, p = -1;
+  if (kind < 2) {
+    rope_pair(j, r0, r.rot, r.style, da, db, p);
+  } else {
+    da = 16 * j + r0;
+    db = da + 8;
+  }
+#pragma unroll
+  for (int i = 0; i < (NB > 1 ? 2 : 1); ++i) {
+    const int col = 2 * q + i;
+    if (col >= nb) continue;
+    float x0 = v[i], x1 = v[2 + i];
+    if (r.bias) {
+      x0 += r.bias[head * r.hd + da];
+      x1 += r.bias[head * r.hd + db];
+    }
+    const int pos = r.positions[col];
+    if (p >= 0) {
+      const float2 cs = *reinterpret_cast<const float2*>(r.rope + ((int64_t)pos * (r.rot / 2) + p) * 2);
+      const float ya = x0 * cs.x - x1 * cs.y, yb = x0 * cs.y + x1 * cs.x;
+      x0 = ya;
+      x1 = yb;
+    }
+    if (kind == 0) {
+      float* dst = r.q + ((int64_t)col * r.nh + head) * r.hd;
+      __stcg(dst + da, x0);
+      __stcg(dst + db, x1);
+    } else {
+      const int kh = head - r.nh - (kind == 2 ? r.nkv : 0);
+      const int blk = r.block_tables[(int64_t)r.row_seq[col] * r.max_blocks + pos / r.block_size];
+      const int64_t row = ((int64_t)blk * r.nkv + kh) * r.block_size + pos % r.block_size;
+      __nv_bfloat16* dst = (kind == 1 ? r.k_cache : r.v_cache) + row * r.hd;
+      dst[da] = __float2bfloat16_rn(x0);
+      dst[db] = __float2bfloat16_rn(x1);
+    }
+  }
+}
+
 }  // namespace mg
 }  // namespace hk

@@ -253,7 +253,11 @@ template <int EPI>
 __device__ __forceinline__ void epilogue(const MgArgs& a, uint32_t g_, const float (&v)[4], int lane) {
   const int64_t g = g_;
   const int r0 = lane >> 2, q = lane & 3;
-  if constexpr (EPI == MG_SWIGLU) {
+  if constexpr (EPI == MG_ROPE) {
+    const RopeEpi r{a.rope, a.positions, a.row_seq, a.block_tables, a.max_blocks, a.block_size, a.k_cache,
+                    a.v_cache, a.q_out, a.bias, a.nh, a.nkv, a.rp_hd, a.rp_rot, a.rp_style};
+    rope_epilogue<2>(r, a.nb, g_, v, lane);
+  } else if constexpr (EPI == MG_SWIGLU) {
     const int64_t o = g * 8 + r0;  // output row: gate in tile row r0, up in r0 + 8
     if (o >= a.F) return;
 #pragma unroll
@@ -531,6 +535,12 @@ void dispatch_epi(int epi, const MgArgs& a, int grid, cudaStream_t st, bool pdl)
     case MG_RESID: dispatch_nb<FMT, MATH, XIN, MG_RESID>(a, grid, st, pdl); break;
     case MG_SWIGLU: dispatch_nb<FMT, MATH, XIN, MG_SWIGLU>(a, grid, st, pdl); break;
     case MG_PUSH: dispatch_nb<FMT, MATH, XIN, MG_PUSH>(a, grid, st, pdl); break;
+    case MG_ROPE:
+      if constexpr (XIN == MG_X_NORM || XIN == MG_X_BF16) {
+        dispatch_nb<FMT, MATH, XIN, MG_ROPE>(a, grid, st, pdl);
+        break;
+      }
+      throw std::runtime_error("mg_gemv: the RoPE epilogue takes fp32 (normalised) or bf16 input");
     default: throw std::runtime_error("mg_gemv: bad epilogue");
   }
 }

@@ -32,6 +32,8 @@ from ..ops import mg
 from .config import ModelConfig
 
 GEMV_COLS = 8  # rows per GEMV launch (dp4a GEMV batch limit)
+# RoPE + paged K/V append in the W4A16 QKV GEMV epilogue where the weights allow it
+ROPE_EPI = os.environ.get("HK_ROPE_EPI", "1") == "1"
 
 
 @dataclass
@@ -313,9 +315,10 @@ class LlamaModel:
             if any(lw.mg_gu is not None for lw in weights.layers):
                 Fm = max(lw.w_down.K for lw in weights.layers if lw.mg_gu is not None)
                 self.hfrag = mg.FragAct(Fm, self.dev) if self.mg_math == "bf16" else mg.IntFragAct(Fm, self.dev)
-        # bs <= 4 decode as one persistent launch (HK_DSTEP=0 keeps the per-kernel path)
+        # bs <= 4 decode as one persistent launch: opt-in (HK_DSTEP=1); measured slower than the
+        # per-kernel path on B200 so far (per-phase barrier, staging and K/V-ring latencies)
         self.dstep = None
-        if os.environ.get("HK_DSTEP", "1") == "1" and self.small_batch == "w4a16":
+        if os.environ.get("HK_DSTEP", "0") == "1" and self.small_batch == "w4a16":
             from ..ops.dstep import DecodeStep
             self.dstep = DecodeStep.build(self)
 
@@ -457,12 +460,14 @@ class LlamaModel:
         if advance:
             ops.advance(inp.ids, self.next_ids, inp.positions, inp.row_ctx, rows)
 
-    def _rope_attention(self, l, lw, rows, splits, out_q8=None, out_bf16=None):
+    def _rope_attention(self, l, lw, rows, splits, out_q8=None, out_bf16=None, roped: bool = False):
+        """RoPE + paged append (unless the QKV GEMV's epilogue did both: ``roped``), then attention."""
         cfg, kv, inp = self.cfg, self.kv, self.inp
-        ops.rope_append(self.qkv[:rows], inp.positions[:rows], None, self.rope, cfg.rope_dim,
-                        cfg.rope_style, self.q[:rows], kv.k[l], kv.v[l], cfg.n_heads, cfg.n_kv_heads,
-                        cfg.head_dim, kv.block_size, bias=lw.qkv_bias, q_norm=lw.q_norm, k_norm=lw.k_norm,
-                        eps=cfg.eps, block_tables=kv.block_tables, row_seq=inp.row_seq[:rows])
+        if not roped:
+            ops.rope_append(self.qkv[:rows], inp.positions[:rows], None, self.rope, cfg.rope_dim,
+                            cfg.rope_style, self.q[:rows], kv.k[l], kv.v[l], cfg.n_heads, cfg.n_kv_heads,
+                            cfg.head_dim, kv.block_size, bias=lw.qkv_bias, q_norm=lw.q_norm, k_norm=lw.k_norm,
+                            eps=cfg.eps, block_tables=kv.block_tables, row_seq=inp.row_seq[:rows])
         if self.long_runs and rows > GEMV_COLS and cfg.head_dim in (64, 128):
             ops.attention_prefill(self.q[:rows], kv.k[l], kv.v[l], kv.block_tables, inp.row_seq[:rows],
                                   inp.row_ctx[:rows], self.scale, out_q8=out_q8, out_bf16=out_bf16)
@@ -472,6 +477,17 @@ class LlamaModel:
                              out_q8=out_q8, out_bf16=out_bf16, counters=self.attn_counters)
 
     # ---- W4A16 small-batch path (ops/mg.py) ----
+    def _rope_in_qkv(self, lw) -> bool:
+        """RoPE and the paged append run in the QKV GEMV epilogue (QKV packed in RoPE-pair
+        order, no per-head q/k norm, whose reduction spans the head; HK_ROPE_EPI=0 turns it off)."""
+        return ROPE_EPI and lw.mg_qkv is not None and lw.mg_qkv.rope is not None and lw.q_norm is None \
+            and lw.k_norm is None
+
+    def _rope_args(self, l, c0, c1):
+        cfg, kv, inp = self.cfg, self.kv, self.inp
+        return (self.rope, inp.positions[c0:c1], inp.row_seq[c0:c1], kv.block_tables, kv.k[l], kv.v[l],
+                self.q[c0:c1], cfg.n_heads, cfg.n_kv_heads, kv.block_size)
+
     def _mg_layer(self, lw) -> bool:
         return self.small_batch == "w4a16" and lw.mg_ready()
 
@@ -480,9 +496,11 @@ class LlamaModel:
         split-KV attention (bf16 out), O projection + residual, fused RMSNorm -> gate/up + SwiGLU
         (h in fragment order), down projection + residual. Five launches per 8 rows."""
         cfg, x, st = self.cfg, self.x, self.status
+        fused = self._rope_in_qkv(lw)
         self._gemv_cols(lambda c0, c1: mg.gemv(lw.mg_qkv, c1 - c0, x_norm=(x[c0:c1], lw.attn_norm, cfg.eps),
-                                               y=self.qkv[c0:c1], status=st), rows)
-        self._rope_attention(l, lw, rows, splits, out_bf16=self.attb[:rows])
+                                               y=self.qkv[c0:c1], status=st,
+                                               rope_append=self._rope_args(l, c0, c1) if fused else None), rows)
+        self._rope_attention(l, lw, rows, splits, out_bf16=self.attb[:rows], roped=fused)
         self._gemv_cols(lambda c0, c1: mg.gemv(lw.mg_o, c1 - c0, xb=self.attb[c0:c1], y=x[c0:c1], residual=True,
                                                status=st), rows)
         if lw.moe is not None:

@@ -55,6 +55,11 @@ class DecodeStep:
         self.counters = torch.zeros(gmax, dtype=torch.int32, device=dev)
         self.bar = torch.zeros(2, dtype=torch.int32, device=dev)
         self.wait_ns = int(os.environ.get("HK_DS_WAIT_NS", "0"))
+        # per CTA: barriers passed, first failed wait (site, phase, warp); read by ``trace_report``
+        self.trace = torch.zeros(self.grid, 4, dtype=torch.int32, device=dev)
+        # per-phase device timestamps (set ``timing = True``; read by ``phase_times``)
+        self.timing = False
+        self.tstamp = torch.zeros(5 * len(model.w.layers) + 2, 4, dtype=torch.int64, device=dev)
 
     @staticmethod
     def eligible(model) -> bool:
@@ -90,13 +95,14 @@ class DecodeStep:
         return ds
 
     def splits(self, rows: int) -> int:
-        """KV splits per (row, KV head): enough items to give every SM one (capped at 32), unless
-        the model forces a split count (speculative verify)."""
+        """KV splits per (row, KV head): items for about a quarter of the SMs (longer splits keep
+        each item's K/V ring busy; fewer partials to merge), capped at 32, unless the model forces
+        a split count (speculative verify)."""
         m = self.model
         if m.force_splits:
             return min(m.force_splits, self.max_splits)
         s = 1
-        while s < self.max_splits and rows * m.cfg.n_kv_heads * s * 2 <= self.grid:
+        while s < self.max_splits and rows * m.cfg.n_kv_heads * s * 4 <= self.grid:
             s *= 2
         return s
 
@@ -111,7 +117,7 @@ class DecodeStep:
 
     def reset(self):
         """Clear the barrier, counters and status after a failed step."""
-        for t in (self.att_cnt, self.h_cnt, self.counters, self.bar):
+        for t in (self.att_cnt, self.h_cnt, self.counters, self.bar, self.trace):
             t.zero_()
 
     def run(self, rows: int, argmax: bool = True):
@@ -125,4 +131,31 @@ class DecodeStep:
             inp.positions, inp.row_seq, inp.row_ctx, kv.block_tables, m.rope, m.x, m.q, kv.k, kv.v,
             self.att_o, self.att_ml, self.att_cnt, self.a_limbs, self.a_info, self.hf, self.h_limbs, self.h_info,
             self.h_cnt, self.part, self.counters, m.w.mg_head.tiles, m.w.out_norm, logits=m.logits,
-            argmax_slots=m.argmax_slots if argmax else None, bar=self.bar, status=m.status, wait_ns=self.wait_ns)
+            argmax_slots=m.argmax_slots if argmax else None, bar=self.bar, status=m.status, wait_ns=self.wait_ns,
+            trace=self.trace, tstamp=self._arm_tstamp() if self.timing else None)
+
+    def _arm_tstamp(self):
+        self.tstamp.zero_()
+        self.tstamp[:, 1] = 2 ** 62  # earliest-arrival column starts high
+        return self.tstamp
+
+    def phase_times(self) -> dict:
+        """Mean microseconds per phase kind over the layers of the last timed step, from CTA 0's
+        barrier exits: ``span`` (barrier to barrier), ``first`` / ``last`` (earliest / latest CTA
+        arrival at the closing barrier, from the opening one), ``stage`` (CTA 0's activation
+        staging, phases that stage)."""
+        t = self.tstamp.cpu().double() / 1000.0
+        L = len(self.model.w.layers)
+        ex = t[:, 0]
+        names = ("qkv_rope", "attention", "o_proj", "gate_up", "down")
+        out = {}
+        for i, n in enumerate(names):
+            rows = torch.arange(L) * 5 + i + 1
+            prev = ex[rows - 1]
+            d = {"span": ex[rows] - prev, "first": t[rows, 1] - prev, "last": t[rows, 2] - prev}
+            if i in (0, 3):
+                d["stage"] = t[rows, 3] - prev
+            out[n] = {k: round(float(v.mean()), 2) for k, v in d.items()}
+        out["lm_head"] = round(float(ex[5 * L + 1] - ex[5 * L]), 2)
+        out["total"] = round(float(ex[5 * L + 1] - ex[0]), 2)
+        return out

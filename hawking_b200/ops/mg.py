@@ -26,7 +26,7 @@ from ..formats.ggml import GgmlType
 from .qweight import QWeight
 
 MG_X_NORM, MG_X_BF16, MG_X_FRAG = 0, 1, 2
-MG_STORE, MG_RESID, MG_SWIGLU, MG_PUSH = 0, 1, 2, 3
+MG_STORE, MG_RESID, MG_SWIGLU, MG_PUSH, MG_ROPE = 0, 1, 2, 3, 4
 MG_FORMATS = (GgmlType.Q4_K,)
 # Math of the packed tiles: "int" (default) takes each activation as 16-bit fixed point per
 # 32-element block (fp32 block scale; two int8 limbs on the u8 x s8 tensor-core MMA; rounding error
@@ -196,13 +196,15 @@ def gemv(mw: MgWeight, nb: int, *, x_norm=None, xb: Optional[torch.Tensor] = Non
          xfrag=None, y: Optional[torch.Tensor] = None, residual: bool = False,
          bias=None, hfrag: Optional[FragAct] = None, hb: Optional[torch.Tensor] = None, argmax_slots=None,
          argmax_offset: int = 0, push=None, status: Optional[torch.Tensor] = None, pdl: Optional[bool] = None,
-         scratch: Optional[MgScratch] = None):
+         scratch: Optional[MgScratch] = None, rope_append=None):
     """One W4A16 GEMV launch over ``nb`` batch columns.
 
     ``x_norm=(x_f32, norm_w, eps)`` (norm_w may be None), ``xb`` or ``xfrag`` (a ``FragAct`` for the
     bf16 math, an ``IntFragAct`` for the integer math) selects the input.
     ``y`` with ``residual`` selects store / add; a SwiGLU-packed weight writes ``hfrag`` / ``hb``;
-    ``push=(recv_table, epoch)`` selects the tensor-parallel push.
+    ``push=(recv_table, epoch)`` selects the tensor-parallel push. ``rope_append=(rope table,
+    positions, row_seq, block_tables, k_cache, v_cache, q_out, nh, nkv, block_size)`` (a QKV matrix
+    packed in RoPE-pair order): RoPE and the paged K/V append in the epilogue, q to q_out.
     """
     from . import PDL, launches
     sc = scratch or MgScratch.get(mw.tiles.device)
@@ -216,6 +218,10 @@ def gemv(mw: MgWeight, nb: int, *, x_norm=None, xb: Optional[torch.Tensor] = Non
         raise ValueError("mg.gemv: an input is required")
     if mw.swiglu:
         epi = MG_SWIGLU
+    elif rope_append is not None:
+        if mw.rope is None:
+            raise ValueError("mg.gemv: the RoPE epilogue needs a matrix packed in RoPE-pair order")
+        epi = MG_ROPE
     elif push is not None:
         epi = MG_PUSH
     else:
@@ -233,4 +239,6 @@ def gemv(mw: MgWeight, nb: int, *, x_norm=None, xb: Optional[torch.Tensor] = Non
         part=sc.part, counters=sc.counters, status=status if status is not None else sc.status,
         pdl=PDL if pdl is None else pdl, math=MATHS[mw.math],
         xinfo=xfrag.info if isinstance(xfrag, IntFragAct) else None,
-        rope_order=list(mw.rope) if mw.rope is not None else [])
+        rope_order=list(mw.rope) if mw.rope is not None else [],
+        rope_epi=list(rope_append[:7]) if rope_append is not None else [],
+        rope_dims=list(rope_append[7:]) if rope_append is not None else [])

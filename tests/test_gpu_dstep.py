@@ -32,7 +32,17 @@ def parts(q4k_path):
 
 
 def _engine(cfg, w):
-    return Engine.build(cfg, w, device="cuda", max_batch=4, max_ctx=512, block_size=16, num_blocks=160, max_rows=16)
+    import os
+    old = os.environ.get("HK_DSTEP")
+    os.environ["HK_DSTEP"] = "1"  # the one-launch step is opt-in
+    try:
+        return Engine.build(cfg, w, device="cuda", max_batch=4, max_ctx=512, block_size=16, num_blocks=160,
+                            max_rows=16)
+    finally:
+        if old is None:
+            del os.environ["HK_DSTEP"]
+        else:
+            os.environ["HK_DSTEP"] = old
 
 
 def _decode_tokens(model, tokens, seq_id):

@@ -206,3 +206,41 @@ def test_mg_in_cuda_graph(math):
         xn = (x * torch.rsqrt((x * x).mean(1, keepdim=True) + 1e-6)).bfloat16()
         _close(y, _ref(w, xn), tol=2e-3)
     _status_ok()
+
+
+@pytest.mark.parametrize("math", MATHS)
+@pytest.mark.parametrize("hd,rot,style,nb", [(128, 128, 0, 1), (128, 128, 1, 3), (64, 64, 0, 8), (128, 64, 1, 2)])
+def test_mg_rope_epilogue_matches_store_then_rope(hd, rot, style, nb, math):
+    """QKV packed in RoPE-pair order: the fused epilogue (bias, RoPE, q out, paged K/V append) equals
+    the logical-order store followed by the stand-alone rope_append kernel."""
+    from hawking_b200 import ops
+    nh, nkv, H, bs = 8, 2, 1024, 16
+    N = (nh + 2 * nkv) * hd
+    w = _w(N, H, hd + rot + style)
+    mw = mg.pack(w, math=math, rope=(nh + nkv, hd, rot, style))
+    x = _x(nb, H, 12)
+    nw = torch.rand(H, device=DEV) + 0.5
+    bias = torch.randn(N, device=DEV) * 0.1
+    rope = ops.rope_table(512, rot, 10000.0, None, DEV)
+    positions = torch.tensor([5 + 37 * i for i in range(nb)], dtype=torch.int32, device=DEV)
+    row_seq = torch.arange(nb, dtype=torch.int32, device=DEV)
+    nblk = nb * 16 + 4
+    tables = torch.randperm(nblk, device=DEV)[: nb * 16].int().view(nb, 16).contiguous()
+    outs = []
+    for fused in (False, True):
+        kc = torch.zeros(nblk, nkv, bs, hd, dtype=torch.bfloat16, device=DEV)
+        vc = torch.zeros_like(kc)
+        q = torch.zeros(nb, nh, hd, device=DEV)
+        y = torch.zeros(nb, N, device=DEV)
+        if fused:
+            mg.gemv(mw, nb, x_norm=(x, nw, 1e-5), y=y, bias=bias,
+                    rope_append=(rope, positions, row_seq, tables, kc, vc, q, nh, nkv, bs))
+        else:
+            mg.gemv(mw, nb, x_norm=(x, nw, 1e-5), y=y)  # logical rows (the store epilogue unpermutes)
+            ops.rope_append(y, positions, None, rope, rot, style, q, kc, vc, nh, nkv, hd, bs, bias=bias,
+                            block_tables=tables, row_seq=row_seq)
+        _status_ok()
+        outs.append((q, kc.float(), vc.float()))
+    for a, b in zip(outs[0], outs[1]):
+        err = (a - b).abs().max().item()
+        assert err <= 1e-2 * b.abs().max().item() + 1e-6, err
