@@ -219,6 +219,7 @@ void attention_decode(const Tensor& q, const Tensor& k_cache, const Tensor& v_ca
   a.counters = optr<int>(counters);
   TORCH_CHECK(!counters.has_value() || counters->numel() >= (int64_t)R * a.nkv, "attention: counters too small");
   a.status = optr<int>(status);
+  a.table_rows = (int)block_tables.size(0);
   const c10::cuda::CUDAGuard g(q.device());
   if (tc && hk::attention_decode_tc_supported(a)) {
     TORCH_CHECK(k_cache.is_contiguous() && v_cache.is_contiguous(), "attention (tensor cores): contiguous caches");

@@ -298,6 +298,7 @@ struct AttnDecodeArgs {
   int* counters;               // [R * nkv] zero-initialised split counters (scratch; reset after use)
   int* status;                 // optional device status word (bounded-wait timeouts)
   int stage_blocks;            // cluster path: KV blocks held in the shared ring (set by the launcher)
+  int table_rows;              // rows of block_tables (0: unknown; bounds the speculative L2 prefetch)
 };
 void attention_decode_launch(const AttnDecodeArgs& a, cudaStream_t s, bool pdl);
 // Cluster variant (num_splits in {1, 2, 4, 8}): the splits of one (row, kv head) merge through
