@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--profile-step", action="store_true",
                     help="run one eager decode step between cudaProfilerStart/Stop (for ncu --profile-from-start off) "
                          "and exit without a result line")
+    ap.add_argument("--flagships", type=int, default=1,
+                    help="also run the DeepSeek-V3-style and Qwen3-Next-style models (sub-objects of the line)")
     ap.add_argument("--one-launch", type=int, default=1,
                     help="also time the opt-in persistent decode step (one launch per step), own key")
     ap.add_argument("--w4a8", type=int, default=1,
@@ -118,9 +120,11 @@ def engine_e2e(eng, vocab: int, prompt_len: int, K: int, W: int, world: int, dev
              "context": prompt_len}, round(ttft, 2))
 
 
-def bench_qwen_next(args):
+def bench_qwen_next(args, sub: bool = False):
     """Qwen3-Next-style hybrid (config 4): bs1 / bs8 device-timed decode on one GPU, 80B-parameter
-    random weights in the mixed <= 1.5 BPW recipe (random codes + Gaussian-statistics scales)."""
+    random weights in the mixed <= 1.5 BPW recipe (random codes + Gaussian-statistics scales).
+    ``sub``: return the result as a dict (a sub-object of the default bench line) instead of
+    printing it."""
     import torch
     from hawking_b200.engine.kv_cache import PagedKVCache
     from hawking_b200.models.config import preset
@@ -129,7 +133,7 @@ def bench_qwen_next(args):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     K, W, ctx = args.steps, args.warmup, args.ctx
-    cfg = preset("qwen3-next", max_ctx=ctx + 2 * (K + W) + 64)
+    cfg = preset("qwen3-next", max_ctx=max(ctx, args.e2e_ctx) + 2 * (K + W) + 64)
     if args.layers:
         cfg = cfg.with_(layers=args.layers)
     t0 = time.time()
@@ -206,6 +210,9 @@ def bench_qwen_next(args):
         "weights_gb": round((w.table.nbytes + w.embed.nbytes) / 1e9, 2),
         "expert_weights_gb": round(expert_bytes / 1e9, 2), "load_s": round(t_load, 1),
     }
+    if sub:
+        m.release_graphs()
+        return out
     print(json.dumps(out))
     return 0
 
@@ -227,10 +234,11 @@ def profile_one_step(m, kv, ctx):
     print(json.dumps({"profile_step": True}))
 
 
-def bench_deepseek(args):
+def bench_deepseek(args, sub: bool = False):
     """DeepSeek-V3-style MLA + MoE (config 5): bs1 / bs8 device-timed decode with random-init fp8
     e4m3 (128 x 128 block-scaled) weights of the full 43-layer architecture; on N > 1 ranks the
-    model is tensor parallel over heads and expert parallel over the 256 experts (parallel/ep.py)."""
+    model is tensor parallel over heads and expert parallel over the 256 experts (parallel/ep.py).
+    ``sub``: run inside the default bench (process group already up; return a dict)."""
     import torch
     import torch.distributed as dist
     from hawking_b200.models.config import preset
@@ -241,11 +249,11 @@ def bench_deepseek(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    if world > 1:
+    if world > 1 and not dist.is_initialized():
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
     K, W, ctx = args.steps, args.warmup, args.ctx
-    cfg = preset("deepseek-v3", max_ctx=ctx + 2 * (K + W) + 64)
+    cfg = preset("deepseek-v3", max_ctx=max(ctx, args.e2e_ctx) + 2 * (K + W) + 64)
     if args.layers:
         cfg = cfg.with_(layers=args.layers)
     t0 = time.time()
@@ -340,6 +348,9 @@ def bench_deepseek(args):
         "bs8": {"tok_s_aggregate": round(8 * 1000.0 / ms8, 1), "ms_per_step": round(ms8, 4), "clocks": clocks8},
         "weights_gb": round(w.nbytes / 1e9, 2), "load_s": round(t_load, 1),
     }
+    if sub:
+        m._graphs.clear()
+        return out
     if rank == 0:
         print(json.dumps(out))
     if world > 1:
@@ -740,15 +751,77 @@ def main():
         tp.check()
         out["tp_collectives"] = "decode (<= 8 rows): GEMV epilogue pushes partials over NVLink + fused " \
                                 "all-reduce/RMSNorm; prefill and bs64 (tensor-core path): NCCL all-reduce"
+    # free the Llama model before the checks and flagship models below
+    m.release_graphs()
+    if tp is not None:
+        tp.close()
+    del eng, m, kv, w
+    import gc
+    gc.collect()
+    torch.cuda.empty_cache()
+    barrier()
+    if use_tp and not args.layers:
+        out["tokens_match_tp1"], out["tokens_agree_prefix"] = tp_token_check(args, world, rank, dev)
+    if args.flagships and not args.layers and args.tp_shard_of <= 1:
+        import copy
+        fa = copy.copy(args)
+        fa.e2e_ctx = 2048  # TTFT at a 2k prompt
+        out["deepseek_v3"] = bench_deepseek(fa, sub=True)
+        gc.collect()
+        torch.cuda.empty_cache()
+        barrier()
+        if world == 1:
+            out["qwen3_next"] = bench_qwen_next(fa, sub=True)
+        else:
+            out["qwen3_next"] = {"unavailable": "Qwen3-Next has no tensor/expert parallelism yet; its 1-GPU "
+                                                "numbers are in the N=1 line"}
+        gc.collect()
+        torch.cuda.empty_cache()
     if rank == 0:
         print(json.dumps(out))
     if world > 1:
-        m.release_graphs()
-        if tp is not None:
-            tp.close()
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def tp_token_check(args, world, rank, dev):
+    """The first 16 greedy ids of a 2-layer model of the bench's architecture (same seed) under
+    N-way tensor parallelism against a one-GPU run on rank 0. Returns (match, agreeing prefix)."""
+    import torch
+    import torch.distributed as dist
+    from hawking_b200.engine.engine import Engine
+    from hawking_b200.engine.sampling import SamplingParams
+    from hawking_b200.formats.synth import random_prompt
+    from hawking_b200.models.config import preset
+    from hawking_b200.models.llama import random_llama_weights
+    from hawking_b200.parallel.tp import TPComm, local_config, shard_llama_weights
+    cfg = preset(args.model).with_(layers=2, max_ctx=512)
+    w = random_llama_weights(cfg, dev, seed=11)  # identical on every rank
+    prompt = random_prompt(24, cfg.vocab, seed=12)
+    sp = SamplingParams(max_tokens=16)
+    ref = []
+    if rank == 0:
+        e1 = Engine.build(cfg, w, device=dev, max_batch=1, max_ctx=512, block_size=64, max_rows=8,
+                          max_prefill_tokens=64, num_blocks=16)
+        ref = e1.generate([prompt], sp)[0]
+        e1.model.release_graphs()
+        del e1
+    dist.barrier()
+    tpc = TPComm(rank, world, 2 * cfg.layers, 8, cfg.hidden, dev)
+    e2 = Engine.build(local_config(cfg, world), shard_llama_weights(w, cfg, rank, world), device=dev, max_batch=1,
+                      max_ctx=512, block_size=64, max_rows=8, max_prefill_tokens=64, num_blocks=16, tp=tpc)
+    got = e2.generate([prompt], sp)[0]
+    tpc.check()
+    e2.model.release_graphs()
+    tpc.close()
+    del e2, w
+    torch.cuda.empty_cache()
+    dist.barrier()
+    n = 0
+    while n < min(len(got), len(ref)) and got[n] == ref[n]:
+        n += 1
+    return (got == ref) if rank == 0 else None, n if rank == 0 else None
 
 
 if __name__ == "__main__":
