@@ -162,8 +162,10 @@ class Engine:
         return Engine.build(cfg, weights, device=device, tp=tp, **config.build_kwargs())
 
     @staticmethod
-    def from_gguf(path: str, device="cuda", max_batch: int = 8, max_ctx: Optional[int] = None, **kw):
-        """Load a GGUF model (weights re-laid for the kernels) and build an engine around it."""
+    def from_gguf(path: str, device="cuda", max_batch: int = 8, max_ctx: Optional[int] = None,
+                  tp_rank: int = 0, tp_world: int = 1, **kw):
+        """Load a GGUF model (weights re-laid for the kernels) and build an engine around it.
+        ``tp_world > 1``: this rank's tensor-parallel shard (the process group must be up)."""
         from ..formats.gguf import GgufModel
         from ..models.llama import load_llama_weights
         from ..models.torch_ref import config_from_gguf
@@ -184,7 +186,14 @@ class Engine:
         torch.cuda.synchronize(device)
         ph["weights"] = (time.perf_counter() - t) * 1e3
         t = time.perf_counter()
-        eng = Engine.build(cfg, w, device=device, max_batch=max_batch, max_ctx=max_ctx, **kw)
+        if tp_world > 1:
+            from ..parallel.tp import TPComm, local_config, shard_llama_weights
+            w = shard_llama_weights(w, cfg, tp_rank, tp_world)
+            tp = TPComm(tp_rank, tp_world, 2 * cfg.layers, 8, cfg.hidden, torch.device(device))
+            eng = Engine.build(local_config(cfg, tp_world), w, device=device, max_batch=max_batch, max_ctx=max_ctx,
+                               tp=tp, **kw)
+        else:
+            eng = Engine.build(cfg, w, device=device, max_batch=max_batch, max_ctx=max_ctx, **kw)
         ph["engine"] = (time.perf_counter() - t) * 1e3
         eng.startup = {k: round(v, 2) for k, v in ph.items()}
         if timing:
@@ -414,34 +423,37 @@ class Engine:
             torch.cuda.current_stream(m.dev).synchronize()
             self.stats.d2h_bytes += 4 * k
             return self._host_ids[:k].tolist()
-        # full-logits lane: device sampler for temperature / top-k / top-p; repetition penalty on host
+        # full-logits lane: device sampler for temperature / top-k / top-p; repetition penalty on host.
+        # Under tensor parallelism the vocabulary slices are gathered first (every rank, same rows).
+        gathered = getattr(m, "gathered_logits", None)
+        logits = gathered(max(r for _, r in rows_here) + 1) if gathered is not None else m.logits
         out = []
         for it, r in rows_here:
             st = self.requests[it.id]
             p = st.params
             if st.json is not None:
-                out.append(self._sample_json(st, m.logits[r]))
+                out.append(self._sample_json(st, logits[r]))
                 continue
             if p.temperature <= 0.0 and p.repetition_penalty == 1.0:
                 torch.cuda.current_stream(m.dev).synchronize()
-                out.append(int(torch.argmax(m.logits[r]).item()))
+                out.append(int(torch.argmax(logits[r]).item()))
                 continue
             if p.repetition_penalty != 1.0:
-                logits = m.logits[r].float().cpu().numpy()
+                row = logits[r].float().cpu().numpy()
                 s = native().Sampler(p.seed)
                 for t in self.sched.tokens(it.id)[-64:]:
                     s.record(t)
                 sp = native().SamplingParams()
                 sp.temperature, sp.top_k, sp.top_p, sp.repetition_penalty = p.temperature, p.top_k, p.top_p, p.repetition_penalty
-                out.append(int(s.sample(logits, sp)))
-                self.stats.d2h_bytes += logits.nbytes
+                out.append(int(s.sample(row, sp)))
+                self.stats.d2h_bytes += row.nbytes
                 continue
             m.temperature[r] = p.temperature
             m.top_k[r] = p.top_k
             m.top_p[r] = p.top_p
             m.uniforms[r] = st.rng.uniform()
             from .. import ops
-            ops.sample(m.logits[r:r + 1], m.temperature[r:r + 1], m.top_k[r:r + 1], m.top_p[r:r + 1], None, None,
+            ops.sample(logits[r:r + 1], m.temperature[r:r + 1], m.top_k[r:r + 1], m.top_p[r:r + 1], None, None,
                        m.uniforms[r:r + 1], m.next_ids[r:r + 1])
             out.append(int(m.next_ids[r].item()))
             self.stats.d2h_bytes += 4

@@ -337,10 +337,24 @@ class DeepSeekModel:
             ops.tp_argmax(tp, self.argmax_slots, rows, self.next_ids)
         elif sample == "none":
             mixed_gemv(w.table, w.lm_head, self.xa.view(rows), self.logits[:rows])
-        else:
-            raise NotImplementedError("tensor-parallel sampling: greedy only")
+        else:  # vocabulary-parallel logits, gathered; every rank draws the same token
+            mixed_gemv(w.table, w.lm_head, self.xa.view(rows), self.logits[:rows])
+            full = self.gathered_logits(rows)
+            ops.sample(full, self.temperature[:rows], self.top_k[:rows], self.top_p[:rows], self.rep_penalty[:rows],
+                       None, self.uniforms[:rows], self.next_ids[:rows])
         if advance:
             ops.advance(inp.ids, self.next_ids, inp.positions, inp.row_ctx, rows)
+
+    def gathered_logits(self, nl: int) -> torch.Tensor:
+        """Logits of the first ``nl`` rows over the whole vocabulary (under tensor parallelism the
+        ranks' vocabulary slices gathered; a collective every rank calls for the same rows)."""
+        if self.tp is None:
+            return self.logits[:nl]
+        from ..parallel.tp import gather_vocab_logits
+        if getattr(self, "_tp_full", None) is None:
+            head = self.w.table.weights[self.w.lm_head]
+            self._tp_full = torch.zeros(self.logits.shape[0], head.N * self.tp.world, device=self.dev)
+        return gather_vocab_logits(self.tp, self.logits[:nl], self._tp_full)
 
     def forward_tokens(self, tokens, seq_id: int = 0, start_pos: int = 0) -> torch.Tensor:
         """Teacher-forced forward of one sequence in chunks of up to 8 rows; fp32 logits [n, vocab]."""

@@ -621,9 +621,13 @@ class LlamaModel:
 
     def _lm_head_tp(self, rows, nl, n_logits, tc, sample):
         w, cfg, tp = self.w, self.cfg, self.tp
-        if sample not in ("greedy", "none"):
-            raise NotImplementedError("tensor-parallel sampling: greedy only")
         if n_logits < 0:
+            return
+        if sample == "sample":  # vocabulary-parallel logits, gathered; every rank draws the same token
+            self._lm_head_tp(rows, nl, n_logits, tc, "none")
+            full = self.gathered_logits(nl)
+            ops.sample(full, self.temperature[:nl], self.top_k[:nl], self.top_p[:nl], self.rep_penalty[:nl], None,
+                       self.uniforms[:nl], self.next_ids[:nl])
             return
         if self.small_batch == "w4a16" and w.mg_head is not None:
             off = tp.rank * w.lm_head.N
@@ -655,6 +659,22 @@ class LlamaModel:
                                                 argmax_slots=self.argmax_slots[c0:c1],
                                                 argmax_offset=tp.rank * w.lm_head.N), nl)
         ops.tp_argmax(tp, self.argmax_slots, nl, self.next_ids)
+
+    def gathered_logits(self, nl: int) -> torch.Tensor:
+        """Logits of the first ``nl`` logit rows over the whole vocabulary: ``self.logits`` on one
+        GPU; under tensor parallelism the ranks' vocabulary slices gathered (a collective: every
+        rank calls it for the same rows)."""
+        if self.tp is None:
+            return self.logits[:nl]
+        from ..parallel.tp import gather_vocab_logits
+        return gather_vocab_logits(self.tp, self.logits[:nl], self._full_logits(nl))
+
+    def _full_logits(self, nl: int) -> torch.Tensor:
+        """[nl, vocab] buffer for the gathered tensor-parallel logits (allocated on first use)."""
+        V = self.w.lm_head.N * self.tp.world
+        if getattr(self, "_tp_full", None) is None or self._tp_full.shape[0] < nl:
+            self._tp_full = torch.zeros(self.max_logit_rows, V, device=self.dev)
+        return self._tp_full[:nl]
 
     def _attention_block_tc(self, l, lw, rows, splits):
         x = self.x[:rows]

@@ -205,3 +205,16 @@ class TPComm:
         with torch.cuda.device(self.dev):
             K.ipc_free(self.base)
         self.closed = True
+
+
+def gather_vocab_logits(tp: "TPComm", local: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    """Vocabulary-parallel logits [rows, V / world] of every rank -> the full logits [rows, V] on
+    every rank (rank r's slice holds vocabulary ids r * V/world ...), so that each rank runs the same
+    sampler on the same distribution with the same uniforms and draws the same token. One NCCL
+    all-gather plus a transposing copy. Parity: crates/hawking-core/src/sample.rs:39-98 (the sampler
+    runs once over the whole vocabulary)."""
+    rows, vs = local.shape
+    buf = torch.empty(tp.world * rows * vs, dtype=local.dtype, device=local.device)
+    dist.all_gather_into_tensor(buf, local.contiguous().view(-1), group=tp.group)
+    out[:rows].view(rows, tp.world, vs).copy_(buf.view(tp.world, rows, vs).transpose(0, 1))
+    return out[:rows]

@@ -1,5 +1,7 @@
 """``python -m hawking_b200.serve --gguf MODEL.gguf [--port 8000]``: serve a GGUF model over the
-OpenAI-compatible HTTP API on one GPU.
+OpenAI-compatible HTTP API. Under ``torch.distributed.run --nproc-per-node N`` the model is
+tensor parallel over the N GPUs (expert parallel for the MoE layers): rank 0 serves HTTP and the
+other ranks step the same schedule in lockstep (``serve/lockstep.py``).
 
 ``--preset deepseek-v3 | qwen3-next | NAME [--layers N]`` serves random-init weights of a named
 architecture instead (the fp8 MLA + MoE model or the `.gravity` hybrid DeltaNet model, which have
@@ -7,6 +9,7 @@ no GGUF of their own here) with the synthetic byte-level tokenizer, or ``--token
 from __future__ import annotations
 
 import argparse
+import os
 
 from .._ext import native
 from ..config import RUNTIME_PROFILES, runtime_profile
@@ -37,32 +40,80 @@ def main(argv=None):
     extra = {k: v for k, v in plan.engine.items() if k not in ("max_batch", "policy")}
     if (args.gguf is None) == (args.preset is None):
         ap.error("give exactly one of --gguf and --preset")
+    world, rank, gloo = init_ranks()
+    device = f"cuda:{int(os.environ.get('LOCAL_RANK', '0'))}" if world > 1 else "cuda"
     if args.gguf:
-        eng = Engine.from_gguf(args.gguf, max_batch=max_batch, max_ctx=args.max_ctx, policy=policy, **extra)
+        eng = Engine.from_gguf(args.gguf, device=device, max_batch=max_batch, max_ctx=args.max_ctx, policy=policy,
+                               tp_rank=rank, tp_world=world, **extra)
         tok = native().Tokenizer.from_gguf(native().GgufFile.open(args.gguf))
         name = args.gguf.rsplit("/", 1)[-1]
     else:
         eng, tok = preset_engine(args.preset, args.layers, max_batch, args.max_ctx, args.tokenizer_gguf,
-                                 policy=policy, **extra)
+                                 device=device, policy=policy, tp_rank=rank, tp_world=world, **extra)
         name = args.preset
     eng.apply_profile(args.profile)
+    if rank > 0:  # follower: the leader's schedule, step for step
+        from .lockstep import follow
+        eng.tokenizer = tok
+        try:
+            follow(eng, gloo)
+        finally:
+            shutdown_ranks(eng)
+        return
+    if world > 1:
+        from .lockstep import LeaderEngine
+        eng = LeaderEngine(eng, gloo)
     loop = ServeLoop(eng, tok, host=args.host, port=args.port, chat_template=args.chat_template,
                      model_id=args.model_id or name, **plan.serve)
     loop.start()
-    print(f"serving {args.gguf} on http://{args.host}:{loop.port}", flush=True)
+    print(f"serving {name} on http://{args.host}:{loop.port}" + (f" over {world} GPUs" if world > 1 else ""),
+          flush=True)
     try:
         loop.run()
     except KeyboardInterrupt:
         pass
     finally:
         loop.stop()
+        if world > 1:
+            eng.stop()
+            shutdown_ranks(eng)
+
+
+def init_ranks():
+    """(world, rank, gloo group) from the torch.distributed.run environment; NCCL for the model's
+    collectives, a gloo group for the lockstep broadcast."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world == 1:
+        return 1, 0, None
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+    return world, dist.get_rank(), dist.new_group(backend="gloo")
+
+
+def shutdown_ranks(eng) -> None:
+    import torch.distributed as dist
+    if not dist.is_initialized():
+        return
+    m = getattr(eng, "model", None)
+    if m is not None and hasattr(m, "release_graphs"):
+        m.release_graphs()
+    tp = getattr(m, "tp", None)
+    dist.barrier()
+    if tp is not None:
+        tp.close()
+    dist.destroy_process_group()
 
 
 def preset_engine(preset: str, layers: int = 0, max_batch: int = 8, max_ctx=None, tokenizer_gguf=None,
-                  device="cuda", policy: int = 0, **build_kw):
+                  device="cuda", policy: int = 0, tp_rank: int = 0, tp_world: int = 1, **build_kw):
     """(Engine, tokenizer) for random-init weights of a named architecture preset. ``build_kw``
     (EngineConfig fields) reach the dense/MoE GGUF-architecture build; the MLA and hybrid engines
-    size their own prefill chunks."""
+    size their own prefill chunks. ``tp_world > 1``: this rank's tensor / expert parallel shard."""
     import os
     import tempfile
 
@@ -73,14 +124,31 @@ def preset_engine(preset: str, layers: int = 0, max_batch: int = 8, max_ctx=None
         cfg = cfg.with_(layers=layers)
     if max_ctx:
         cfg = cfg.with_(max_ctx=max_ctx)
+    import torch
+    dev = torch.device(device)
     if cfg.arch == "deepseek2":
-        from ..models.deepseek import random_deepseek_weights
-        eng = Engine.build_deepseek(cfg, random_deepseek_weights(cfg, device), device=device, max_batch=max_batch,
-                                    policy=policy)
+        if tp_world > 1:
+            from ..parallel.ep import local_deepseek_config, random_deepseek_weights_ep
+            from ..parallel.tp import TPComm
+            tp = TPComm(tp_rank, tp_world, 2 * cfg.layers, 8, cfg.hidden, dev)
+            eng = Engine.build_deepseek(local_deepseek_config(cfg, tp_world),
+                                        random_deepseek_weights_ep(cfg, tp_rank, tp_world, dev), device=device,
+                                        max_batch=max_batch, policy=policy, tp=tp)
+        else:
+            from ..models.deepseek import random_deepseek_weights
+            eng = Engine.build_deepseek(cfg, random_deepseek_weights(cfg, device), device=device, max_batch=max_batch,
+                                        policy=policy)
     elif cfg.arch == "qwen3next":
+        if tp_world > 1:
+            raise ValueError("qwen3-next serves on one GPU (no tensor / expert parallelism yet)")
         from ..models.qwen_next import random_qwen_next_weights
         eng = Engine.build_qwen_next(cfg, random_qwen_next_weights(cfg, device), device=device, max_batch=max_batch,
                                      policy=policy)
+    elif tp_world > 1:
+        from ..parallel.tp import TPComm, local_config, random_llama_weights_tp
+        tp = TPComm(tp_rank, tp_world, 2 * cfg.layers, 8, cfg.hidden, dev)
+        eng = Engine.build(local_config(cfg, tp_world), random_llama_weights_tp(cfg, tp_rank, tp_world, dev),
+                           device=device, max_batch=max_batch, policy=policy, tp=tp, **build_kw)
     else:
         from ..models.llama import random_llama_weights
         eng = Engine.build(cfg, random_llama_weights(cfg, device), device=device, max_batch=max_batch, policy=policy,

@@ -194,3 +194,55 @@ def test_tp2_q4k_w4a16_push_matches_tp1(math, tmp_path):
     assert r["err"] < 0.01, r
     assert r["gens"][0] == r["gens"][1]  # every rank decodes the same tokens
     assert [g[0] for g in r["gens"][0]] == [g[0] for g in r["ref_gen"]], r
+
+
+def _sampling_worker(rank, world, port, out_path):
+    """Non-greedy decode under tensor parallelism: gathered vocabulary slices, same uniforms."""
+    import datetime
+
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        from hawking_b200.engine.engine import Engine
+        from hawking_b200.engine.sampling import SamplingParams
+        from hawking_b200.models.config import preset
+        from hawking_b200.models.llama import random_llama_weights
+        from hawking_b200.parallel.tp import TPComm, local_config, shard_llama_weights
+        cfg = preset("llama3-8b", layers=2, hidden=1024, n_heads=8, n_kv_heads=2, ffn=2048, vocab=2048, max_ctx=128)
+        w = random_llama_weights(cfg, dev, seed=6, std=0.08)
+        tp = TPComm(rank, world, 2 * cfg.layers, 8, cfg.hidden, dev)
+        eng = Engine.build(local_config(cfg, world), shard_llama_weights(w, cfg, rank, world), device=dev,
+                           max_batch=4, max_ctx=128, block_size=16, num_blocks=64, max_rows=8, tp=tp)
+        sp = SamplingParams(max_tokens=12, temperature=0.9, top_k=40, top_p=0.95, seed=123)
+        gen = eng.generate([list(range(30, 40))], sp)
+        gens = [None] * world
+        dist.all_gather_object(gens, gen)
+        tp.check()
+        if rank == 0:
+            ref = Engine.build(cfg, w, device=dev, max_batch=4, max_ctx=128, block_size=16, num_blocks=64,
+                               max_rows=8)
+            ref_gen = ref.generate([list(range(30, 40))], sp)
+            greedy = ref.generate([list(range(30, 40))], SamplingParams(max_tokens=12))
+            torch.save({"gens": gens, "ref_gen": ref_gen, "greedy": greedy}, out_path)
+        torch.cuda.synchronize()
+        tp.close()
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp2_sampling_matches_tp1(tmp_path):
+    import torch.multiprocessing as mp
+    out = str(tmp_path / "sample.pt")
+    mp.spawn(_sampling_worker, args=(2, _free_port(), out), nprocs=2, join=True)
+    r = torch.load(out)
+    assert r["gens"][0] == r["gens"][1]  # every rank draws the same tokens
+    assert r["gens"][0] == r["ref_gen"], r  # and the one-GPU engine draws them too (same seed)
+    assert r["ref_gen"] != r["greedy"], r  # it really sampled
