@@ -23,6 +23,7 @@ void bind_engine(py::module_& m) {
       .def("table", &BlockManager::table)
       .def("slots", &BlockManager::slots)
       .def("attach_prefix", &BlockManager::attach_prefix)
+      .def("cached_prefix", &BlockManager::cached_prefix)
       .def("commit_prefix", &BlockManager::commit_prefix)
       .def("fork", &BlockManager::fork)
       .def("truncate", &BlockManager::truncate)
@@ -58,6 +59,7 @@ void bind_engine(py::module_& m) {
       .def("abort", &Scheduler::abort)
       .def("schedule", &Scheduler::schedule)
       .def("commit", &Scheduler::commit)
+      .def("commit_run", &Scheduler::commit_run, py::arg("id"), py::arg("toks"), py::arg("computed"))
       .def_property_readonly("num_waiting", &Scheduler::num_waiting)
       .def_property_readonly("num_running", &Scheduler::num_running)
       .def("idle", &Scheduler::idle)

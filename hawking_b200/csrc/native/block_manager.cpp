@@ -133,6 +133,24 @@ int BlockManager::attach_prefix(int64_t seq, const std::vector<int>& tokens) {
   return s.tokens;
 }
 
+int BlockManager::cached_prefix(const std::vector<int>& tokens) const {
+  if (!prefix_cache_) return 0;
+  const int max_full = ((int)tokens.size() - 1) / bs_;
+  uint64_t h = 1469598103934665603ull;
+  int n = 0;
+  for (int i = 0; i < max_full; ++i) {
+    h = mix(h, tokens.data() + i * bs_, bs_);
+    auto ix = index_.find(h);
+    if (ix == index_.end()) break;
+    const auto& info = block_info_.at(ix->second);
+    bool same = true;
+    for (int k = 0; k < bs_ && same; ++k) same = info.toks[k] == tokens[i * bs_ + k];
+    if (!same) break;
+    n += bs_;
+  }
+  return n;
+}
+
 void BlockManager::commit_prefix(int64_t seq, const std::vector<int>& tokens, int n_valid) {
   if (!prefix_cache_) return;
   const auto& t = table(seq);

@@ -40,6 +40,9 @@ class BlockManager {
   // number of tokens covered (a multiple of block_size, at most tokens.size() - 1 so at least
   // one token is always computed).
   int attach_prefix(int64_t seq, const std::vector<int>& tokens);
+  // Tokens of `tokens` that attach_prefix would find cached (whole blocks, at least one token left
+  // to compute), without attaching anything.
+  int cached_prefix(const std::vector<int>& tokens) const;
   // Register the full blocks of seq holding tokens[0:n_valid] in the prefix index.
   void commit_prefix(int64_t seq, const std::vector<int>& tokens, int n_valid);
   // Share src's blocks with dst. Full blocks are shared; a partial last block is copied: the

@@ -169,6 +169,32 @@ std::vector<StepEvent> Scheduler::commit(const StepPlan& plan, const std::vector
   return ev;
 }
 
+std::vector<StepEvent> Scheduler::commit_run(int64_t id, const std::vector<int>& toks, int computed) {
+  std::vector<StepEvent> ev;
+  auto rit = reqs_.find(id);
+  if (rit == reqs_.end()) return ev;
+  auto& r = rit->second;
+  if (r.state != ReqState::Decoding) throw std::runtime_error("scheduler commit_run: request is not decoding");
+  r.computed = std::max(r.computed, computed);
+  for (int tok : toks) {
+    r.tokens.push_back(tok);
+    r.generated += 1;
+    int fin = 0;
+    if (std::find(r.stop.begin(), r.stop.end(), tok) != r.stop.end()) fin = (int)FinishReason::Stop;
+    else if (r.generated >= r.max_new || (int)r.tokens.size() >= r.max_context) fin = (int)FinishReason::Length;
+    ev.push_back(StepEvent{id, tok, fin});
+    if (fin) {
+      finish(r);
+      break;
+    }
+  }
+  if (r.state == ReqState::Finished) {
+    reqs_.erase(rit);
+    order_.erase(std::remove(order_.begin(), order_.end(), id), order_.end());
+  }
+  return ev;
+}
+
 int Scheduler::num_waiting() const {
   int n = 0;
   for (const auto& kv : reqs_) n += kv.second.state == ReqState::Waiting;

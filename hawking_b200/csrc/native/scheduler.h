@@ -57,6 +57,10 @@ class Scheduler {
   bool abort(int64_t id);
   StepPlan schedule();
   std::vector<StepEvent> commit(const StepPlan& plan, const std::vector<int>& sampled);
+  // Speculative decoding: the decoding request `id` emitted `toks` (accepted drafts plus the
+  // verifier's token) and its KV now covers `computed` tokens. Stop ids and length end the run
+  // early; one event per emitted token.
+  std::vector<StepEvent> commit_run(int64_t id, const std::vector<int>& toks, int computed);
 
   int num_waiting() const;
   int num_running() const;

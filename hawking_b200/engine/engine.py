@@ -92,6 +92,8 @@ class Engine:
         self.ledger: List[dict] = []
         self.profile = "default"
         self.startup: Dict[str, float] = {}  # load phases in ms (Engine.from_gguf)
+        self.spec = None  # speculative decoding in the step (enable_speculative)
+        self.prefix_disk = None  # disk prefix-KV reuse at admission (enable_prefix_disk)
 
     # ---- construction helpers ----
     @staticmethod
@@ -200,10 +202,67 @@ class Engine:
             print(json.dumps({"startup_ms": eng.startup, "path": path}), file=sys.stderr, flush=True)
         return eng
 
+    # ---- disk prefix-KV reuse ----
+    def enable_prefix_disk(self, directory: str, min_blocks: int = 4, max_entries: int = 64):
+        """At admission, a prompt whose longest whole-block prefix is not in the in-memory prefix
+        cache but is on disk (a KV snapshot keyed by the SHA-256 of the prefix's token ids) has the
+        snapshot loaded into cache blocks and registered as a cached prefix, so the scheduler
+        attaches it like any in-memory hit. When a prompt's prefill completes, its longest
+        whole-block prefix of at least ``min_blocks`` blocks is written to disk (LRU over
+        ``max_entries`` files). Attention-only KV caches (no recurrent state).
+
+        Parity: crates/hawking-core/src/cache/prefill_disk.rs:1-45 (rolling-hash prefix keys,
+        longest-prefix lookup, LRU), crates/hawking-serve/src/http.rs:206-263 (lookup at admission)."""
+        from .checkpoint import PrefixDiskCache
+        self.prefix_disk = PrefixDiskCache(directory, max_entries)
+        self._pd_min = max(1, min_blocks) * self.kv.block_size
+        self._pd_pending: Dict[int, int] = {}  # request id -> prefix length to store after prefill
+        self.stats_disk = {"hits": 0, "hit_tokens": 0, "stored": 0}
+
+    def _prefix_from_disk(self, prompt: List[int]) -> None:
+        kv, bs = self.kv, self.kv.block_size
+        have = kv.bm.cached_prefix(prompt)
+        top = (len(prompt) - 1) // bs * bs
+        for n in range(top, max(have, self._pd_min - 1), -bs):
+            path = self.prefix_disk._path(prompt[:n])
+            if not os.path.exists(path):
+                continue
+            from .checkpoint import load_sequence
+            tmp = -next(self._ids)
+            try:
+                toks = load_sequence(kv, tmp, path)  # sha256 of the payload verified on read
+                kv.bm.commit_prefix(tmp, toks, len(toks))
+                os.utime(path)  # LRU touch
+                self.stats_disk["hits"] += 1
+                self.stats_disk["hit_tokens"] += n
+            except (ValueError, RuntimeError):
+                pass  # a corrupt or foreign snapshot is a miss
+            finally:
+                kv.drop(tmp)
+            return
+
+    def _prefix_to_disk(self, events) -> None:
+        """After a step: store the prompt prefix of requests whose prefill just completed."""
+        for rid, n in list(self._pd_pending.items()):
+            if self.sched.state(rid) != 2:  # not decoding yet (or gone)
+                if self.sched.state(rid) == 3:
+                    self._pd_pending.pop(rid, None)
+                continue
+            self._pd_pending.pop(rid, None)
+            toks = list(self.sched.tokens(rid))[:n]
+            path = self.prefix_disk._path(toks)
+            if not os.path.exists(path) and self.kv.bm.num_tokens(rid) >= n:
+                self.prefix_disk.store(self.kv, rid, toks)
+                self.stats_disk["stored"] += 1
+
     # ---- requests ----
     def add_request(self, prompt: List[int], params: Optional[SamplingParams] = None) -> int:
         params = params or SamplingParams()
+        if self.prefix_disk is not None and len(prompt) > self._pd_min:
+            self._prefix_from_disk(list(map(int, prompt)))
         rid = next(self._ids)
+        if self.prefix_disk is not None and len(prompt) > self._pd_min:
+            self._pd_pending[rid] = (len(prompt) - 1) // self.kv.block_size * self.kv.block_size
         self.sched.add(rid, list(map(int, prompt)), params.max_tokens, params.greedy, list(params.stop_ids),
                        self.cfg.max_ctx)
         st = RequestState(rid, params, RequestRng(params.seed), t_arrival=time.perf_counter())
@@ -224,12 +283,113 @@ class Engine:
     def has_work(self) -> bool:
         return not self.sched.idle()
 
+    # ---- speculative decoding inside the step ----
+    def enable_speculative(self, k: int = 4, min_accept_rate: float = 0.2):
+        """Steps that decode exactly one greedy request run a speculative cycle instead: an n-gram
+        draft of up to ``k`` tokens from the request's own history, verified by one forward of
+        ``k + 1`` rows, the accepted tokens plus the verifier's next token committed at once. The
+        output is bitwise the plain greedy output (attention splits pinned to the single-row
+        count, per-row GEMV math independent of the row count). A governor turns drafting off
+        while acceptance stays low. ``k = 0`` disables it.
+
+        Parity: crates/hawking-core/src/model/qwen_dense.rs:1986-2010 (speculation inside the
+        decode loop), crates/hawking-serve/src/spec_gov.rs:13-90 (governor)."""
+        m = self.model
+        if k <= 0:
+            self.spec = None
+            return
+        n = native()
+        self.spec = {"k": max(1, min(k, n.MAX_VERIFY_BATCH - 1, m.max_rows - 1)),
+                     "gov": n.SpecGovernor(16, min_accept_rate), "drafts": {}, "cycles": 0, "drafted": 0,
+                     "accepted": 0, "emitted": 0}
+        if hasattr(m, "num_splits"):
+            m.force_splits = m.num_splits(1)
+            if hasattr(m, "release_graphs"):
+                m.release_graphs()
+
+    def _spec_eligible(self, items) -> bool:
+        if self.spec is None or len(items) != 1:
+            return False
+        it = items[0]
+        st = self.requests.get(it.id)
+        return bool(it.sample and it.greedy and it.p1 - it.p0 == 1 and st is not None and st.json is None
+                    and not getattr(self.model, "serial_rows", False))
+
+    def _spec_step(self, it) -> List[tuple]:
+        sp, m, kv = self.spec, self.model, self.kv
+        toks = list(self.sched.tokens(it.id))
+        d = sp["drafts"].get(it.id)
+        if d is None:
+            d = sp["drafts"][it.id] = native().NgramDraft()
+            d.warm_start(toks)
+        p = it.p0  # the last token's position (its KV is computed by this forward)
+        k = min(sp["k"], self.requests[it.id].params.max_tokens - (len(toks) - self.sched.prompt_len(it.id)) - 1)
+        draft = list(d.propose(toks[-2:], k)) if k > 0 and sp["gov"].enabled else []
+        rows = [toks[-1]] + draft
+        if not kv.bm.reserve(it.id, p + len(rows)):
+            draft, rows = [], [toks[-1]]  # no room for the draft: a plain decode row
+        kv.sync_tables([it.id])
+        r = kv.row(it.id)
+        slots = kv.bm.slots(it.id, p, p + len(rows))
+        pos = list(range(p, p + len(rows)))
+        self.stats.h2d_bytes += m.inp.upload(rows, pos, slots, [r] * len(rows), [q + 1 for q in pos])
+        if hasattr(m, "long_runs"):
+            m.long_runs = False
+        m.forward(len(rows), "greedy")
+        n = len(rows)
+        self._host_ids[:n].copy_(m.next_ids[:n], non_blocking=True)
+        torch.cuda.current_stream(m.dev).synchronize()
+        self.stats.d2h_bytes += 4 * n
+        verifier = self._host_ids[:n].tolist()
+        self._check_device_status()
+        emit, a = native().accept_draft(draft, verifier)
+        kv.bm.truncate(it.id, p + 1 + a)
+        events = self.sched.commit_run(it.id, list(emit), p + 1 + a)
+        for e in events:
+            d.note_token(int(e.token))
+        sp["cycles"] += 1
+        sp["drafted"] += len(draft)
+        sp["accepted"] += a
+        sp["emitted"] += len(events)
+        if draft:
+            sp["gov"].step(a > 0)
+        else:
+            sp["gov"].tick_disabled()
+        self.stats.steps += 1
+        self.stats.decode_rows += n
+        self.stats.tokens_generated += len(events)
+        now = time.perf_counter()
+        out = []
+        for e in events:
+            out.append((e.id, e.token, e.finish))
+            st = self.requests.get(e.id)
+            if st is not None:
+                st.output.append(e.token)
+                if st.t_first is None:
+                    st.t_first = now
+                if e.finish:
+                    st.finish = e.finish
+                    st.t_done = now
+                    self.kv.drop(e.id)
+                    sp["drafts"].pop(e.id, None)
+        return out
+
+    def spec_stats(self) -> Optional[dict]:
+        sp = self.spec
+        if sp is None:
+            return None
+        return {k: sp[k] for k in ("k", "cycles", "drafted", "accepted", "emitted")} | {
+            "accept_rate": round(sp["accepted"] / sp["drafted"], 3) if sp["drafted"] else 0.0,
+            "tokens_per_cycle": round(sp["emitted"] / sp["cycles"], 3) if sp["cycles"] else 0.0}
+
     # ---- one step ----
     def step(self) -> List[tuple]:
         """Run one scheduler step. Returns [(request_id, token, finish_reason)] for sampled rows."""
         t0 = time.perf_counter()
         with trace("engine.step"):
             out = self._step()
+        if self.prefix_disk is not None and self._pd_pending:
+            self._prefix_to_disk(out)
         self.stats.step_s += time.perf_counter() - t0
         return out
 
@@ -273,6 +433,8 @@ class Engine:
         items = plan.items
         if not items:
             return []
+        if self._spec_eligible(items):
+            return self._spec_step(items[0])
         m = self.model
         ids, pos, slots, rseq, rctx, sample_rows = [], [], [], [], [], []
         live = [it.id for it in items]

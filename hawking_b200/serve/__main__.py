@@ -30,6 +30,10 @@ def main(argv=None):
     ap.add_argument("--max-ctx", type=int, default=None)
     ap.add_argument("--chat-template", default="auto", choices=["auto", "llama3", "chatml", "deepseek", "generic"])
     ap.add_argument("--policy", type=int, default=None, help="0 default, 1 greedy-first, 2 prefix-grouped")
+    ap.add_argument("--spec", type=int, default=0,
+                    help="speculative decoding: n-gram drafts of up to K tokens when one greedy request decodes")
+    ap.add_argument("--prefix-disk", default=None,
+                    help="directory of prompt-prefix KV snapshots reused at admission (per rank under TP)")
     ap.add_argument("--profile", default="default", choices=sorted(RUNTIME_PROFILES),
                     help="runtime profile (lever plan): " + "; ".join(p.contract for p in RUNTIME_PROFILES.values()))
     args = ap.parse_args(argv)
@@ -52,6 +56,10 @@ def main(argv=None):
                                  device=device, policy=policy, tp_rank=rank, tp_world=world, **extra)
         name = args.preset
     eng.apply_profile(args.profile)
+    if args.spec:
+        eng.enable_speculative(args.spec)
+    if args.prefix_disk:
+        eng.enable_prefix_disk(os.path.join(args.prefix_disk, f"rank{rank}") if world > 1 else args.prefix_disk)
     if rank > 0:  # follower: the leader's schedule, step for step
         from .lockstep import follow
         eng.tokenizer = tok
