@@ -31,6 +31,9 @@ def _cmd_generate(a) -> int:
         from .engine.engine import Engine
         eng = Engine.from_gguf(a.gguf, max_batch=1, max_ctx=a.max_ctx, **extra)
         tok = native().Tokenizer.from_gguf(native().GgufFile.open(a.gguf))
+    elif a.model:
+        from .serve.__main__ import path_engine
+        eng, tok = path_engine(a.model, 1, a.max_ctx, a.tokenizer_gguf, **extra)
     else:
         from .serve.__main__ import preset_engine
         eng, tok = preset_engine(a.preset, a.layers, 1, a.max_ctx, **extra)
@@ -171,6 +174,8 @@ def main(argv: Optional[List[str]] = None) -> int:
     sub.add_parser("serve", help="OpenAI-compatible HTTP server")
     g = sub.add_parser("generate", help="generate text for one prompt")
     g.add_argument("--gguf")
+    g.add_argument("--model", help="a GGUF file or a .gravity artifact (container sniffed)")
+    g.add_argument("--tokenizer-gguf", default=None, help="with --model: the tokenizer of a .gravity artifact")
     g.add_argument("--preset")
     g.add_argument("--layers", type=int, default=0)
     g.add_argument("--prompt", required=True)
@@ -202,8 +207,8 @@ def main(argv: Optional[List[str]] = None) -> int:
     if rest:
         ap.error("unrecognized arguments: " + " ".join(rest))
     if a.cmd == "generate":
-        if bool(a.gguf) == bool(a.preset):
-            ap.error("give exactly one of --gguf and --preset")
+        if sum(map(bool, (a.gguf, a.preset, a.model))) != 1:
+            ap.error("give exactly one of --gguf, --model and --preset")
         return _cmd_generate(a)
     return {"tokenize": _cmd_tokenize, "info": _cmd_info, "verify": _cmd_verify, "doctor": _cmd_doctor,
             "version": _cmd_version}[a.cmd](a)

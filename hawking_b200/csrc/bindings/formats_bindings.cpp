@@ -248,6 +248,15 @@ void bind_formats(py::module_& m) {
   m.def("encode_hgravu01", [](py::array_t<float, py::array::c_style | py::array::forcecast> w, int group, int bits) {
     return to_np(encode_hgravu01(w.data(), (int)w.shape(0), (int)w.shape(1), group, bits));
   });
+  m.def("wrap_hgravb01", [](int rows, int cols, int group, py::array_t<uint8_t, py::array::c_style> scales,
+                            py::array_t<uint8_t, py::array::c_style> signs) {
+    return to_np(wrap_hgravb01(rows, cols, group, scales.data(), (size_t)scales.size(), signs.data(), (size_t)signs.size()));
+  });
+  m.def("wrap_hgravu01", [](int rows, int cols, int group, int bits, py::array_t<uint8_t, py::array::c_style> scales,
+                            py::array_t<uint8_t, py::array::c_style> codes) {
+    return to_np(wrap_hgravu01(rows, cols, group, bits, scales.data(), (size_t)scales.size(), codes.data(),
+                               (size_t)codes.size()));
+  });
   m.def("encode_hgravr02", [](py::array_t<float, py::array::c_style | py::array::forcecast> w, int group, double ratio,
                               uint32_t k) {
     return to_np(encode_hgravr02(w.data(), (int)w.shape(0), (int)w.shape(1), group, ratio, k));

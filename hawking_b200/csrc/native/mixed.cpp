@@ -309,6 +309,42 @@ std::vector<float> decode_mixed(const uint8_t* d, size_t n, int* rows, int* cols
   fail("mixed: unknown payload magic " + e.magic);
 }
 
+namespace {
+Json binary_header(int rows, int cols, int group, size_t sign_bytes) {
+  const size_t el = (size_t)rows * cols, groups = el / group;
+  Json h = Json::object();
+  h.set("schema", Json::string(kSchemaBinary));
+  h.set("shape", shape2(rows, cols));
+  h.set("elements", Json::uinteger(el));
+  h.set("group_size", Json::uinteger(group));
+  h.set("groups", Json::uinteger(groups));
+  h.set("scale_bytes", Json::uinteger(groups * 2));
+  h.set("sign_bytes", Json::uinteger(sign_bytes));
+  return h;
+}
+}  // namespace
+
+std::vector<uint8_t> wrap_hgravb01(int rows, int cols, int group, const uint8_t* scales, size_t scale_bytes,
+                                   const uint8_t* signs, size_t sign_bytes) {
+  if (group <= 0 || cols % group) fail("HGRAVB01 wrap: cols must be a multiple of group");
+  const size_t el = (size_t)rows * cols, groups = el / group;
+  if (scale_bytes != groups * 2 || sign_bytes != (el + 7) / 8) fail("HGRAVB01 wrap: plane sizes do not match the shape");
+  std::vector<uint8_t> body(scales, scales + scale_bytes);
+  body.insert(body.end(), signs, signs + sign_bytes);
+  return envelope("HGRAVB01", binary_header(rows, cols, group, sign_bytes), body);
+}
+
+std::vector<uint8_t> wrap_hgravu01(int rows, int cols, int group, int bits, const uint8_t* scales,
+                                   size_t scale_bytes, const uint8_t* codes, size_t code_bytes) {
+  if (bits < 2 || bits > 8 || group <= 0 || cols % group) fail("HGRAVU01 wrap: bad geometry");
+  const size_t el = (size_t)rows * cols, groups = el / group;
+  if (scale_bytes != groups * 2 || code_bytes != (groups * group * bits + 7) / 8)
+    fail("HGRAVU01 wrap: plane sizes do not match the shape");
+  std::vector<uint8_t> body(scales, scales + scale_bytes);
+  body.insert(body.end(), codes, codes + code_bytes);
+  return envelope("HGRAVU01", uniform_header(rows, cols, group, bits), body);
+}
+
 std::vector<uint8_t> encode_hgravb01(const float* w, int rows, int cols, int group) {
   if (cols % group) fail("HGRAVB01 encode: cols must be a multiple of group");
   const size_t el = (size_t)rows * cols, groups = el / group;
@@ -322,15 +358,7 @@ std::vector<uint8_t> encode_hgravb01(const float* w, int rows, int cols, int gro
   for (size_t e = 0; e < el; ++e)
     if (w[e] >= 0) signs[e >> 3] |= (uint8_t)(1u << (e & 7));
   body.insert(body.end(), signs.begin(), signs.end());
-  Json h = Json::object();
-  h.set("schema", Json::string(kSchemaBinary));
-  h.set("shape", shape2(rows, cols));
-  h.set("elements", Json::uinteger(el));
-  h.set("group_size", Json::uinteger(group));
-  h.set("groups", Json::uinteger(groups));
-  h.set("scale_bytes", Json::uinteger(groups * 2));
-  h.set("sign_bytes", Json::uinteger(signs.size()));
-  return envelope("HGRAVB01", h, body);
+  return envelope("HGRAVB01", binary_header(rows, cols, group, signs.size()), body);
 }
 
 std::vector<uint8_t> encode_hgravu01(const float* w, int rows, int cols, int group, int bits) {

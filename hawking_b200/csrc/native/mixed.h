@@ -69,6 +69,12 @@ std::vector<float> decode_mixed(const uint8_t* data, size_t n, int* rows, int* c
 // Encoders (synthetic artifacts). Inputs are row-major fp32 [rows, cols].
 std::vector<uint8_t> encode_hgravb01(const float* w, int rows, int cols, int group);
 std::vector<uint8_t> encode_hgravu01(const float* w, int rows, int cols, int group, int bits);
+// Envelopes around planes that are already quantised (fp16 group scales, then the LSB-first sign or
+// code stream), with no re-quantisation: the artifact writer of models quantised on the device.
+std::vector<uint8_t> wrap_hgravb01(int rows, int cols, int group, const uint8_t* scales, size_t scale_bytes,
+                                   const uint8_t* signs, size_t sign_bytes);
+std::vector<uint8_t> wrap_hgravu01(int rows, int cols, int group, int bits, const uint8_t* scales,
+                                   size_t scale_bytes, const uint8_t* codes, size_t code_bytes);
 std::vector<uint8_t> encode_hgravr02(const float* w, int rows, int cols, int group, double outlier_ratio,
                                      uint32_t rice_k);
 std::vector<uint8_t> encode_hgravs01(const float* left, const float* right, int out, int rank, int in, int group,

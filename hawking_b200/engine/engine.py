@@ -164,6 +164,32 @@ class Engine:
         return Engine.build(cfg, weights, device=device, tp=tp, **config.build_kwargs())
 
     @staticmethod
+    def from_path(path: str, device="cuda", max_batch: int = 8, max_ctx: Optional[int] = None, verify: bool = True,
+                  **kw):
+        """Open a model file or artifact by its container: a `.gravity` artifact directory of the
+        Qwen3-Next hybrid (payload sha256s verified once at admission when ``verify``), or a GGUF
+        file (``from_gguf``).
+
+        Parity: crates/hawking-core/src/model/mod.rs:120-171 (load_engine: container sniff, then
+        the architecture switch)."""
+        from ..formats.gravity import is_gravity
+        if is_gravity(path):
+            from ..models import qwen_next_artifact as qa
+            if not qa.is_artifact(path):
+                raise ValueError(f"{path}: a .gravity artifact of an architecture this build does not load from files")
+            cfg, w = qa.load(path, device, verify=verify)
+            if max_ctx:
+                cfg = cfg.with_(max_ctx=max_ctx)
+            return Engine.build_qwen_next(cfg, w, device=device, max_batch=max_batch,
+                                          **{k: v for k, v in kw.items() if k in ("block_size", "num_blocks",
+                                                                                  "kv_fraction", "policy")})
+        with open(path, "rb") as f:
+            magic = f.read(4)
+        if magic == b"GGUF":
+            return Engine.from_gguf(path, device=device, max_batch=max_batch, max_ctx=max_ctx, **kw)
+        raise ValueError(f"{path}: neither a GGUF file nor a .gravity artifact")
+
+    @staticmethod
     def from_gguf(path: str, device="cuda", max_batch: int = 8, max_ctx: Optional[int] = None,
                   tp_rank: int = 0, tp_world: int = 1, **kw):
         """Load a GGUF model (weights re-laid for the kernels) and build an engine around it.

@@ -20,6 +20,7 @@ from .server import ServeLoop
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--gguf", default=None)
+    ap.add_argument("--model", default=None, help="a GGUF file or a .gravity artifact (container sniffed)")
     ap.add_argument("--preset", default=None, help="serve random-init weights of this architecture preset")
     ap.add_argument("--layers", type=int, default=0, help="with --preset: override the layer count")
     ap.add_argument("--tokenizer-gguf", default=None, help="with --preset: the tokenizer (default: synthetic)")
@@ -42,8 +43,8 @@ def main(argv=None):
     max_batch = args.max_batch if args.max_batch is not None else int(plan.engine.get("max_batch", 8))
     policy = args.policy if args.policy is not None else int(plan.engine.get("policy", 0))
     extra = {k: v for k, v in plan.engine.items() if k not in ("max_batch", "policy")}
-    if (args.gguf is None) == (args.preset is None):
-        ap.error("give exactly one of --gguf and --preset")
+    if sum(x is not None for x in (args.gguf, args.preset, args.model)) != 1:
+        ap.error("give exactly one of --gguf, --model and --preset")
     world, rank, gloo = init_ranks()
     device = f"cuda:{int(os.environ.get('LOCAL_RANK', '0'))}" if world > 1 else "cuda"
     if args.gguf:
@@ -51,6 +52,12 @@ def main(argv=None):
                                tp_rank=rank, tp_world=world, **extra)
         tok = native().Tokenizer.from_gguf(native().GgufFile.open(args.gguf))
         name = args.gguf.rsplit("/", 1)[-1]
+    elif args.model:
+        if world > 1:
+            ap.error("--model serves on one GPU (use --gguf or --preset under tensor parallelism)")
+        eng, tok = path_engine(args.model, max_batch, args.max_ctx, args.tokenizer_gguf, device=device,
+                               policy=policy, **extra)
+        name = os.path.basename(os.path.normpath(args.model))
     else:
         eng, tok = preset_engine(args.preset, args.layers, max_batch, args.max_ctx, args.tokenizer_gguf,
                                  device=device, policy=policy, tp_rank=rank, tp_world=world, **extra)
@@ -115,6 +122,29 @@ def shutdown_ranks(eng) -> None:
     if tp is not None:
         tp.close()
     dist.destroy_process_group()
+
+
+def path_engine(path: str, max_batch: int = 8, max_ctx=None, tokenizer_gguf=None, device="cuda", policy: int = 0,
+                **build_kw):
+    """(Engine, tokenizer) for a model file or artifact (``Engine.from_path``): a GGUF brings its
+    own tokenizer; a `.gravity` artifact takes ``tokenizer_gguf``'s or the synthetic byte-level
+    one over its vocabulary."""
+    import tempfile
+
+    from ..formats.synth import write_tokenizer_gguf
+    eng = Engine.from_path(path, device=device, max_batch=max_batch, max_ctx=max_ctx, policy=policy, **build_kw)
+    tp = tokenizer_gguf
+    if tp is None:
+        is_gguf = False
+        if not os.path.isdir(path):
+            with open(path, "rb") as f:
+                is_gguf = f.read(4) == b"GGUF"
+        if is_gguf:
+            tp = path
+        else:
+            tp = os.path.join(tempfile.mkdtemp(prefix="hk-tok-"), "tokenizer.gguf")
+            write_tokenizer_gguf(tp, eng.cfg.vocab)
+    return eng, native().Tokenizer.from_gguf(native().GgufFile.open(tp))
 
 
 def preset_engine(preset: str, layers: int = 0, max_batch: int = 8, max_ctx=None, tokenizer_gguf=None,
