@@ -248,6 +248,44 @@ void bind_formats(py::module_& m) {
   m.def("encode_hgravu01", [](py::array_t<float, py::array::c_style | py::array::forcecast> w, int group, int bits) {
     return to_np(encode_hgravu01(w.data(), (int)w.shape(0), (int)w.shape(1), group, bits));
   });
+  // Planes of the residual / low-rank codecs for the device GEMVs (ops/mixed.py).
+  m.def("hgravr02_parts", [](py::array_t<uint8_t, py::array::c_style> a) {
+    auto r = parse_hgravr02(a.data(), a.size());
+    py::dict d;
+    d["rows"] = r.base.rows;
+    d["cols"] = r.base.cols;
+    d["group"] = r.base.group;
+    std::vector<uint8_t> sc(r.base.scales.size() * 2);
+    std::memcpy(sc.data(), r.base.scales.data(), sc.size());
+    d["scales"] = to_np(sc);
+    d["signs"] = to_np(r.base.signs);
+    py::array_t<uint32_t> idx(r.indices.size());
+    std::memcpy(idx.mutable_data(), r.indices.data(), r.indices.size() * 4);
+    d["indices"] = idx;
+    d["residual_scale"] = fp16_to_f32(r.residual_scale);
+    d["residual_signs"] = to_np(r.residual_signs);
+    return d;
+  });
+  m.def("hgravs01_parts", [](py::array_t<uint8_t, py::array::c_style> a) {
+    auto lr = parse_hgravs01(a.data(), a.size());
+    auto factor = [](const UniformGroup& u) {
+      py::dict f;
+      f["rows"] = u.rows;
+      f["cols"] = u.cols;
+      f["group"] = u.group;
+      f["bits"] = u.bits;
+      std::vector<uint8_t> sc(u.scales.size() * 2);
+      std::memcpy(sc.data(), u.scales.data(), sc.size());
+      f["scales"] = to_np(sc);
+      f["codes"] = to_np(u.codes);
+      return f;
+    };
+    py::dict d;
+    d["rank"] = lr.rank;
+    d["left"] = factor(lr.left);
+    d["right"] = factor(lr.right);
+    return d;
+  });
   m.def("wrap_hgravb01", [](int rows, int cols, int group, py::array_t<uint8_t, py::array::c_style> scales,
                             py::array_t<uint8_t, py::array::c_style> signs) {
     return to_np(wrap_hgravb01(rows, cols, group, scales.data(), (size_t)scales.size(), signs.data(), (size_t)signs.size()));

@@ -367,8 +367,28 @@ void mla_out(const Tensor& o_lat, const Tensor& w_uv, const Tensor& oq, const Te
 }
 }  // namespace
 
+namespace {
+void sparse_residual(const Tensor& row_ptr, const Tensor& cols, const Tensor& signs, double scale, int64_t N,
+                     const Tensor& xq, const Tensor& xd, int64_t K, int64_t nb, const Tensor& y, bool pdl) {
+  TORCH_CHECK(row_ptr.is_cuda() && row_ptr.scalar_type() == at::kInt && row_ptr.numel() == N + 1,
+              "sparse_residual: row_ptr int32 [N + 1]");
+  TORCH_CHECK(cols.scalar_type() == at::kInt && signs.scalar_type() == at::kChar && cols.numel() == signs.numel(),
+              "sparse_residual: cols int32 / signs int8 [nnz]");
+  TORCH_CHECK(xq.scalar_type() == at::kChar && xq.is_contiguous() && xq.numel() >= nb * K && xd.numel() >= nb * K / 32,
+              "sparse_residual: q8 activations [nb, K]");
+  TORCH_CHECK(y.scalar_type() == at::kFloat && y.stride(-1) == 1 && y.size(0) >= nb && y.size(-1) >= N,
+              "sparse_residual: y fp32 [nb, >= N]");
+  const c10::cuda::CUDAGuard g(y.device());
+  hk::sparse_residual_launch(row_ptr.data_ptr<int>(), cols.data_ptr<int>(), signs.data_ptr<int8_t>(), (float)scale,
+                             (int)N, xq.data_ptr<int8_t>(), xd.data_ptr<float>(), (int)K, (int)nb, y.data_ptr<float>(),
+                             y.stride(0), at::cuda::getCurrentCUDAStream().stream(), pdl);
+}
+}  // namespace
+
 namespace hk {
 void register_model_kernels(py::module_& m) {
+  m.def("sparse_residual", &sparse_residual, py::arg("row_ptr"), py::arg("cols"), py::arg("signs"), py::arg("scale"),
+        py::arg("N"), py::arg("xq"), py::arg("xd"), py::arg("K"), py::arg("nb"), py::arg("y"), py::arg("pdl") = false);
   m.def("mla_kv_append", &mla_kv_append, py::arg("kv_a"), py::arg("norm_w"), py::arg("eps"), py::arg("positions"),
         py::arg("block_tables"), py::arg("row_seq"), py::arg("rope"), py::arg("cache"), py::arg("pdl") = false);
   m.def("mla_absorb_q", &mla_absorb_q, py::arg("q"), py::arg("w_uk"), py::arg("positions"), py::arg("rope"),

@@ -500,6 +500,10 @@ struct MixedGemvArgs {
   int64_t argmax_offset;
 };
 void mixed_gemv_launch(int epi, const MixedGemvArgs& a, cudaStream_t s, bool pdl);
+// HGRAVR02 outlier residual added into y [nb, >= N] (row_ptr [N + 1], cols / signs [nnz]).
+void sparse_residual_launch(const int* row_ptr, const int* cols, const int8_t* signs, float scale, int N,
+                            const int8_t* xq, const float* xd, int K, int nb, float* y, int64_t y_stride,
+                            cudaStream_t s, bool pdl);
 struct MoeMixedArgs {
   const MixedDesc* desc;      // expert e of matrix m at desc_base_m + e
   int desc_base0, desc_base1;

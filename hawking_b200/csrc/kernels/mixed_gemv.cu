@@ -326,6 +326,46 @@ __global__ void moe_active_kernel(const int* counts, int E, int* active, int* n_
   pdl_launch();
 }
 
+// ---- HGRAVR02 outlier residual (the binary base runs on the mixed GEMV) -----------------------
+// y[b, n] += s * sum_j sign_j * x[b, col_j] over the outliers j of row n (CSR built at load from the
+// Rice-coded flat indices). One warp per output row, lanes over the row's outliers in a fixed
+// order, a fixed warp reduction: deterministic. x is the q8 activation blocks of the GEMV.
+__global__ void __launch_bounds__(256) sparse_residual_kernel(const int* row_ptr, const int* cols,
+                                                              const int8_t* signs, float s, int N, const int8_t* xq,
+                                                              const float* xd, int K, int nb, float* y,
+                                                              int64_t y_stride) {
+  pdl_wait();
+  const int n = (int)((blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+  if (n < N) {
+    const int j0 = row_ptr[n], j1 = row_ptr[n + 1];
+    float acc[8];
+#pragma unroll
+    for (int b = 0; b < 8; ++b) acc[b] = 0.f;
+    for (int j = j0 + lane; j < j1; j += 32) {
+      const int c = cols[j];
+      const float sg = (float)signs[j];
+#pragma unroll
+      for (int b = 0; b < 8; ++b)
+        if (b < nb) acc[b] += sg * (float)xq[(int64_t)b * K + c] * xd[(int64_t)b * (K / 32) + c / 32];
+    }
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+      if (b >= nb) break;
+      const float v = warp_sum(acc[b]);
+      if (lane == 0) y[(int64_t)b * y_stride + n] += s * v;
+    }
+  }
+  pdl_launch();
+}
+
+void sparse_residual_launch(const int* row_ptr, const int* cols, const int8_t* signs, float scale, int N,
+                            const int8_t* xq, const float* xd, int K, int nb, float* y, int64_t y_stride,
+                            cudaStream_t s, bool pdl) {
+  if (nb < 1 || nb > 8 || K % 32) throw std::runtime_error("sparse_residual: 1..8 rows, K % 32 == 0");
+  launch(sparse_residual_kernel, dim3((unsigned)((N + 7) / 8)), dim3(256), 0, s, pdl, row_ptr, cols, signs, scale, N,
+         xq, xd, K, nb, y, y_stride);
+}
+
 void moe_active_launch(const int* counts, int E, int* active, int* n_active, cudaStream_t s, bool pdl) {
   launch(moe_active_kernel, dim3(1), dim3(512), 0, s, pdl, counts, E, active, n_active);
 }

@@ -239,3 +239,127 @@ def mixed_gemv_swiglu(table: MixedTable, i_gate: int, i_up: int, x, out):
     launches.add()
     kernels().mixed_gemv(EPI_SWIGLU_Q8, table.descs, i_gate, i_up, w.N, w.K, x.q, x.d, x.s, None, 1.0, out.q, out.d,
                          out.s, PDL, None)
+
+
+@dataclass
+class RiceResidualWeight:
+    """HGRAVR02 on the device: the binary base (a MixedWeight) plus the outlier residual as CSR
+    rows (columns and +-1 signs of each row's outliers, one fp16-derived rms scale)."""
+    base: MixedWeight
+    row_ptr: torch.Tensor   # int32 [N + 1]
+    cols: torch.Tensor      # int32 [nnz]
+    signs: torch.Tensor     # int8 [nnz]
+    scale: float
+
+    @property
+    def N(self) -> int:
+        return self.base.N
+
+    @property
+    def K(self) -> int:
+        return self.base.K
+
+    @property
+    def nbytes(self) -> int:
+        return self.base.nbytes + self.cols.numel() * 4 + self.signs.numel() + self.row_ptr.numel() * 4
+
+    @staticmethod
+    def from_payload(payload: np.ndarray, device) -> "RiceResidualWeight":
+        from .._ext import native
+        p = native().hgravr02_parts(np.ascontiguousarray(payload, dtype=np.uint8))
+        N, K, gs = int(p["rows"]), int(p["cols"]), int(p["group"])
+        scales = torch.from_numpy(np.asarray(p["scales"]).copy().view(np.float16).reshape(N, K // gs))
+        codes = torch.from_numpy(np.asarray(p["signs"]).copy().reshape(N, K // 8))
+        base = MixedWeight(BINARY, 1, gs, N, K, codes.to(device).contiguous(), scales.to(device).contiguous())
+        idx = np.asarray(p["indices"]).astype(np.int64)
+        rows, cols = idx // K, idx % K
+        rs = np.asarray(p["residual_signs"])
+        bits = (rs[np.arange(len(idx)) >> 3] >> (np.arange(len(idx)) & 7)) & 1
+        order = np.lexsort((cols, rows))  # rows, then columns (the flat indices are already ascending)
+        row_ptr = np.zeros(N + 1, dtype=np.int32)
+        np.add.at(row_ptr, rows + 1, 1)
+        row_ptr = np.cumsum(row_ptr).astype(np.int32)
+        t = lambda a, dt: torch.from_numpy(np.ascontiguousarray(a, dtype=dt)).to(device)  # noqa: E731
+        return RiceResidualWeight(base, t(row_ptr, np.int32), t(cols[order], np.int32),
+                                  t(np.where(bits[order] > 0, 1, -1), np.int8), float(p["residual_scale"]))
+
+    def dequantize(self) -> torch.Tensor:
+        w = self.base.dequantize()
+        rp = self.row_ptr.cpu().tolist()
+        for n in range(self.N):
+            for j in range(rp[n], rp[n + 1]):
+                w[n, int(self.cols[j])] += self.scale * float(self.signs[j])
+        return w
+
+
+@dataclass
+class LowRankWeight:
+    """HGRAVS01 on the device: W ~= L @ R with both factors uniform-group MixedWeights; y = L (R x),
+    the rank-wide intermediate re-quantised to int8 blocks between the two GEMVs."""
+    left: MixedWeight    # [N, rank]
+    right: MixedWeight   # [rank, K]
+
+    @property
+    def N(self) -> int:
+        return self.left.N
+
+    @property
+    def K(self) -> int:
+        return self.right.K
+
+    @property
+    def rank(self) -> int:
+        return self.right.N
+
+    @property
+    def nbytes(self) -> int:
+        return self.left.nbytes + self.right.nbytes
+
+    @staticmethod
+    def from_payload(payload: np.ndarray, device) -> "LowRankWeight":
+        from .._ext import native
+        p = native().hgravs01_parts(np.ascontiguousarray(payload, dtype=np.uint8))
+
+        def factor(f) -> MixedWeight:
+            r, c, gs, bits = int(f["rows"]), int(f["cols"]), int(f["group"]), int(f["bits"])
+            if c % gs:
+                raise ValueError("HGRAVS01 on the device: factor groups must tile the rows")
+            sc = torch.from_numpy(np.asarray(f["scales"]).copy().view(np.float16).reshape(r, c // gs))
+            codes = torch.from_numpy(np.asarray(f["codes"]).copy().reshape(r, c * bits // 8))
+            return MixedWeight(UNIFORM, bits, gs, r, c, codes.to(device).contiguous(), sc.to(device).contiguous())
+
+        return LowRankWeight(factor(p["left"]), factor(p["right"]))
+
+    def dequantize(self) -> torch.Tensor:
+        return self.left.dequantize() @ self.right.dequantize()
+
+
+_SINGLE_TABLES: dict = {}
+
+
+def _table_of(w: MixedWeight) -> MixedTable:
+    t = _SINGLE_TABLES.get(id(w))
+    if t is None or t.weights[0] is not w:
+        t = _SINGLE_TABLES[id(w)] = MixedTable([w])
+    return t
+
+
+def mixed_linear(w, x, y: torch.Tensor, residual: bool = False):
+    """y (+)= W x for one `.gravity` weight of any device codec (binary / uniform: one GEMV;
+    HGRAVR02: the base GEMV then the outlier residual; HGRAVS01: R x, re-quantised, then L)."""
+    from . import PDL, Q8Act, launches, rmsnorm_q8
+    rows = x.q.shape[0]
+    if isinstance(w, MixedWeight):
+        mixed_gemv(_table_of(w), 0, x, y, residual=residual)
+    elif isinstance(w, RiceResidualWeight):
+        mixed_gemv(_table_of(w.base), 0, x, y, residual=residual)
+        launches.add()
+        kernels().sparse_residual(w.row_ptr, w.cols, w.signs, w.scale, w.N, x.q, x.d, w.K, rows, y, PDL)
+    elif isinstance(w, LowRankWeight):
+        t = torch.zeros(rows, w.rank, device=y.device)
+        mixed_gemv(_table_of(w.right), 0, x, t)
+        tq = Q8Act(rows, w.rank, y.device)
+        rmsnorm_q8(t, None, 0.0, tq, norm=False)
+        mixed_gemv(_table_of(w.left), 0, tq, y, residual=residual)
+    else:
+        raise TypeError(f"mixed_linear: {type(w).__name__}")

@@ -31,3 +31,22 @@ def test_wrap_round_trip(kind, bits):
 def test_wrap_rejects_wrong_plane_sizes():
     with pytest.raises(Exception):
         native().wrap_hgravu01(4, 64, 64, 4, np.zeros(8, np.uint8), np.zeros(3, np.uint8))
+
+
+def test_r02_s01_device_planes_match_cpu_decode():
+    """The planes the device GEMVs use (binary base + CSR outliers; the two low-rank factors)
+    reconstruct the C++ decode of the payload."""
+    from hawking_b200.formats import mixed as mx
+    from hawking_b200.ops.mixed import LowRankWeight, RiceResidualWeight
+    rng = np.random.default_rng(1)
+    w = (rng.standard_normal((96, 512)) * 0.05).astype(np.float32)
+    w[rng.random((96, 512)) < 0.01] *= 12
+    p = mx.encode_binary_residual(w, group=128, ratio=0.02, rice_k=5)
+    rw = RiceResidualWeight.from_payload(p, "cpu")
+    assert rw.cols.numel() > 0 and int(rw.row_ptr[-1]) == rw.cols.numel()
+    assert np.array_equal(rw.dequantize().numpy(), mx.decode(p))
+    L = (rng.standard_normal((128, 64)) * 0.1).astype(np.float32)
+    R = (rng.standard_normal((64, 512)) * 0.1).astype(np.float32)
+    p = mx.encode_low_rank(L, R, bits=4, group=64)
+    lw = LowRankWeight.from_payload(p, "cpu")
+    assert np.allclose(lw.dequantize().numpy(), mx.decode(p), rtol=1e-5, atol=1e-6)
