@@ -54,6 +54,8 @@ def parse():
                          "and exit without a result line")
     ap.add_argument("--flagships", type=int, default=1,
                     help="also run the DeepSeek-V3-style and Qwen3-Next-style models (sub-objects of the line)")
+    ap.add_argument("--artifact", type=int, default=1,
+                    help="Qwen3-Next: write the weights as a .gravity artifact and decode from the loaded artifact")
     ap.add_argument("--one-launch", type=int, default=1,
                     help="also time the opt-in persistent decode step (one launch per step), own key")
     ap.add_argument("--w4a8", type=int, default=1,
@@ -139,6 +141,27 @@ def bench_qwen_next(args, sub: bool = False):
     t0 = time.time()
     w = random_qwen_next_weights(cfg, dev, seed=0)
     t_load = time.time() - t0
+    artifact = None
+    if args.artifact:
+        # through a `.gravity` artifact: written with the repo's writer, read back (every payload's
+        # sha256 verified once at admission) and decoded from the loaded planes
+        import shutil
+        import tempfile
+        from hawking_b200.models import qwen_next_artifact as qa
+        d = tempfile.mkdtemp(prefix="hk-qn-artifact-")
+        try:
+            t1 = time.time()
+            idx = qa.save(d, cfg, w)
+            t2 = time.time()
+            del w
+            torch.cuda.empty_cache()
+            cfg2, w = qa.load(d, dev, verify=True)
+            t3 = time.time()
+            artifact = {"shards": len(set(idx["weight_map"].values())), "tensors": len(idx["weight_map"]),
+                        "bytes": sum(os.path.getsize(os.path.join(d, f)) for f in os.listdir(d)),
+                        "write_s": round(t2 - t1, 1), "load_verify_s": round(t3 - t2, 1)}
+        finally:
+            shutil.rmtree(d, ignore_errors=True)
     n_full = sum(cfg.layer_is_full_attention(l) for l in range(cfg.layers))
     bs, max_seqs = 64, 8
     max_blocks = -(-cfg.max_ctx // bs)
@@ -209,6 +232,7 @@ def bench_qwen_next(args, sub: bool = False):
         "bs8": {"tok_s_aggregate": round(8 * 1000.0 / ms8, 1), "ms_per_step": round(ms8, 4), "clocks": clocks8},
         "weights_gb": round((w.table.nbytes + w.embed.nbytes) / 1e9, 2),
         "expert_weights_gb": round(expert_bytes / 1e9, 2), "load_s": round(t_load, 1),
+        "artifact": artifact or "in-memory weights (--artifact 0)",
     }
     if sub:
         m.release_graphs()

@@ -36,7 +36,17 @@ py::array_t<uint8_t> to_np(const std::vector<uint8_t>& v) {
 }  // namespace
 
 void bind_formats(py::module_& m) {
-  m.def("sha256_hex", [](py::array_t<uint8_t, py::array::c_style> a) { return Sha256::hex_of(a.data(), a.size()); });
+  m.def("sha256_hex", [](py::array_t<uint8_t, py::array::c_style> a) {
+    const uint8_t* p = a.data();
+    const size_t n = (size_t)a.size();
+    py::gil_scoped_release unlocked;  // callers hash several files on threads
+    return Sha256::hex_of(p, n);
+  });
+  m.def("sha256_hex_portable", [](py::array_t<uint8_t, py::array::c_style> a) {
+    Sha256 h(true);
+    h.update(a.data(), (size_t)a.size());
+    return h.hex();
+  });
   m.def("canonical_json", [](py::handle o) { return from_py(o).canonical(); });
   m.def("json_number", &json_number);
 

@@ -1,6 +1,9 @@
 // `.gravity` container; see gravity.h.
 #include "gravity.h"
 
+#include <atomic>
+#include <thread>
+
 #include <fcntl.h>
 #include <sys/mman.h>
 #include <sys/stat.h>
@@ -86,6 +89,25 @@ const GravityTensor* GravityShard::find(const std::string& name) const {
   return it == index_.end() ? nullptr : &tensors_[it->second];
 }
 
+namespace {
+// Runs f(i) for i in [0, n) on up to hardware_concurrency threads (payload hashing).
+template <typename F>
+void parallel_for(size_t n, F f) {
+  const size_t nt = std::max<size_t>(1, std::min<size_t>(n, std::thread::hardware_concurrency()));
+  if (nt <= 1) {
+    for (size_t i = 0; i < n; ++i) f(i);
+    return;
+  }
+  std::atomic<size_t> next{0};
+  std::vector<std::thread> ts;
+  for (size_t t = 0; t < nt; ++t)
+    ts.emplace_back([&]() {
+      for (size_t i = next++; i < n; i = next++) f(i);
+    });
+  for (auto& t : ts) t.join();
+}
+}  // namespace
+
 bool GravityShard::verify_tensor(const std::string& name) const {
   const auto* t = find(name);
   if (!t) throw std::runtime_error("gravity: no tensor " + name);
@@ -112,12 +134,17 @@ Json GravityShard::verify() const {
   if (layout_err.empty() && cursor != phys)
     layout_err = "trailing or undeclared body bytes: declared " + std::to_string(cursor) + ", physical " +
                  std::to_string(phys);
-  const std::string body_hex = Sha256::hex_of(base_ + body_off_, phys);
+  std::string body_hex;
+  std::vector<char> tensor_ok(ord.size(), 0);
+  std::thread body_thread([&]() { body_hex = Sha256::hex_of(base_ + body_off_, phys); });
+  parallel_for(ord.size(), [&](size_t i) { tensor_ok[i] = Sha256::hex_of(data(*ord[i]), ord[i]->bytes) == ord[i]->sha256; });
+  body_thread.join();
   const bool body_ok = body_hex == header_.pointer("/integrity/body_sha256").as_string();
   Json bad = Json::array(), empty = Json::array();
   uint64_t el_all = 0, by_all = 0, el_cmp = 0, by_cmp = 0;
-  for (const auto* t : ord) {
-    if (Sha256::hex_of(data(*t), t->bytes) != t->sha256) bad.push(Json::string(t->name));
+  for (size_t i = 0; i < ord.size(); ++i) {
+    const auto* t = ord[i];
+    if (!tensor_ok[i]) bad.push(Json::string(t->name));
     if (t->bytes == 0) empty.push(Json::string(t->name));
     if (t->elements) {
       el_all += t->elements;
@@ -149,18 +176,29 @@ void GravityWriter::add(Json d, const uint8_t* data, size_t n) {
 }
 
 Json GravityWriter::write(const std::string& path) const {
-  Sha256 body;
   Json tensors = Json::array();
   std::set<std::string> seen;
+  // the body digest (one stream) on its own thread, the payload digests in parallel
+  std::string body_hex;
+  std::thread body_thread([&]() {
+    Sha256 body;
+    for (const auto& it : items_) body.update(it.second.data(), it.second.size());
+    body_hex = body.hex();
+  });
+  std::vector<std::string> digests(items_.size());
+  parallel_for(items_.size(), [&](size_t i) {
+    digests[i] = Sha256::hex_of(items_[i].second.data(), items_[i].second.size());
+  });
+  body_thread.join();
   uint64_t off = 0;
-  for (const auto& it : items_) {
+  for (size_t i = 0; i < items_.size(); ++i) {
+    const auto& it = items_[i];
     Json e = it.first;
     const std::string name = e["name"].as_string();
     if (!name.empty() && !seen.insert(name).second) throw std::runtime_error("gravity writer: duplicate tensor " + name);
-    body.update(it.second.data(), it.second.size());
     e.set("offset", Json::uinteger(off));
     e.set("bytes", Json::uinteger(it.second.size()));
-    e.set("sha256", Json::string(Sha256::hex_of(it.second.data(), it.second.size())));
+    e.set("sha256", Json::string(digests[i]));
     tensors.push(std::move(e));
     off += it.second.size();
   }
@@ -171,7 +209,7 @@ Json GravityWriter::write(const std::string& path) const {
   for (const char* k : {"model", "architecture", "tokenizer", "compression", "shard", "gguf_metadata"})
     h.set(k, meta_or(k));
   Json integ = Json::object();
-  integ.set("body_sha256", Json::string(body.hex()));
+  integ.set("body_sha256", Json::string(body_hex));
   integ.set("tensor_count", Json::uinteger(items_.size()));
   h.set("integrity", integ);
   h.set("tensors", tensors);

@@ -4,6 +4,9 @@
 
 #include <algorithm>
 #include <cstring>
+#if defined(__x86_64__)
+#include <immintrin.h>
+#endif
 
 namespace hk {
 
@@ -48,6 +51,61 @@ void Sha256::block(const uint8_t* p) {
   h_[0] += a; h_[1] += b; h_[2] += c; h_[3] += d; h_[4] += e; h_[5] += f; h_[6] += g; h_[7] += h;
 }
 
+#if defined(__x86_64__)
+namespace {
+// The compression function on the x86 SHA extensions. State held as (A B E F) and (C D G H);
+// sha256rnds2 runs two rounds on the low two dwords of W + K; sha256msg1 / msg2 extend the message
+// schedule (sigma0 and sigma1 terms), four words at a time.
+__attribute__((target("sha,sse4.1,ssse3"))) void blocks_shani(uint32_t h[8], const uint8_t* p, size_t nblocks) {
+  const __m128i bswap = _mm_set_epi64x(0x0c0d0e0f08090a0bULL, 0x0405060700010203ULL);
+  __m128i t = _mm_shuffle_epi32(_mm_loadu_si128(reinterpret_cast<const __m128i*>(h)), 0xB1);
+  __m128i s1 = _mm_shuffle_epi32(_mm_loadu_si128(reinterpret_cast<const __m128i*>(h + 4)), 0x1B);
+  __m128i s0 = _mm_alignr_epi8(t, s1, 8);  // A B E F
+  s1 = _mm_blend_epi16(s1, t, 0xF0);       // C D G H
+  for (; nblocks; --nblocks, p += 64) {
+    const __m128i save0 = s0, save1 = s1;
+    __m128i w[4];
+    for (int i = 0; i < 4; ++i)
+      w[i] = _mm_shuffle_epi8(_mm_loadu_si128(reinterpret_cast<const __m128i*>(p + 16 * i)), bswap);
+    for (int i = 0; i < 16; ++i) {
+      if (i >= 4) {  // W[4i .. 4i + 3] from the four previous groups
+        __m128i x = _mm_sha256msg1_epu32(w[(i - 4) & 3], w[(i - 3) & 3]);
+        x = _mm_add_epi32(x, _mm_alignr_epi8(w[(i - 1) & 3], w[(i - 2) & 3], 4));
+        w[i & 3] = _mm_sha256msg2_epu32(x, w[(i - 1) & 3]);
+      }
+      __m128i m = _mm_add_epi32(w[i & 3], _mm_loadu_si128(reinterpret_cast<const __m128i*>(K + 4 * i)));
+      s1 = _mm_sha256rnds2_epu32(s1, s0, m);
+      m = _mm_shuffle_epi32(m, 0x0E);
+      s0 = _mm_sha256rnds2_epu32(s0, s1, m);
+    }
+    s0 = _mm_add_epi32(s0, save0);
+    s1 = _mm_add_epi32(s1, save1);
+  }
+  t = _mm_shuffle_epi32(s0, 0x1B);    // F E B A
+  s1 = _mm_shuffle_epi32(s1, 0xB1);   // D C H G
+  s0 = _mm_blend_epi16(t, s1, 0xF0);  // D C B A
+  s1 = _mm_alignr_epi8(s1, t, 8);     // H G F E
+  _mm_storeu_si128(reinterpret_cast<__m128i*>(h), s0);
+  _mm_storeu_si128(reinterpret_cast<__m128i*>(h + 4), s1);
+}
+bool have_shani() {
+  static const bool ok = __builtin_cpu_supports("sha") && __builtin_cpu_supports("sse4.1") &&
+                         __builtin_cpu_supports("ssse3");
+  return ok;
+}
+}  // namespace
+#endif
+
+void Sha256::blocks(const uint8_t* p, size_t n) {
+#if defined(__x86_64__)
+  if (!portable_ && have_shani()) {
+    blocks_shani(h_, p, n);
+    return;
+  }
+#endif
+  for (size_t i = 0; i < n; ++i) block(p + 64 * i);
+}
+
 void Sha256::update(const void* data, size_t n) {
   const uint8_t* p = static_cast<const uint8_t*>(data);
   total_ += n;
@@ -55,9 +113,13 @@ void Sha256::update(const void* data, size_t n) {
     size_t take = std::min(n, 64 - blen_);
     std::memcpy(buf_ + blen_, p, take);
     blen_ += take; p += take; n -= take;
-    if (blen_ == 64) { block(buf_); blen_ = 0; }
+    if (blen_ == 64) { blocks(buf_, 1); blen_ = 0; }
   }
-  while (n >= 64) { block(p); p += 64; n -= 64; }
+  if (n >= 64) {
+    blocks(p, n / 64);
+    p += n / 64 * 64;
+    n %= 64;
+  }
   if (n) { std::memcpy(buf_, p, n); blen_ = n; }
 }
 

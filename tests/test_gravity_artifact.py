@@ -50,3 +50,13 @@ def test_r02_s01_device_planes_match_cpu_decode():
     p = mx.encode_low_rank(L, R, bits=4, group=64)
     lw = LowRankWeight.from_payload(p, "cpu")
     assert np.allclose(lw.dequantize().numpy(), mx.decode(p), rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("size", [0, 1, 55, 56, 63, 64, 65, 127, 128, 1000, 4113, 1 << 20])
+def test_sha256_paths_agree(size):
+    """The SHA-extension compression path, the portable one and hashlib give the same digest."""
+    import hashlib
+    a = np.random.default_rng(size).integers(0, 256, size=size, dtype=np.uint8)
+    want = hashlib.sha256(a.tobytes()).hexdigest()
+    assert native().sha256_hex(a) == want
+    assert native().sha256_hex_portable(a) == want
