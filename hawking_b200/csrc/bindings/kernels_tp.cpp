@@ -115,7 +115,58 @@ void tp_argmax(const Tensor& slots, int64_t rows, int64_t max_rows, const Tensor
 }  // namespace
 
 namespace hk {
+// Non-owning tensor over raw device memory (an IPC allocation) of `numel` fp32 elements.
+Tensor wrap_f32(int64_t ptr, int64_t numel, int64_t device) {
+  return at::from_blob(as_ptr<void>(ptr), {numel}, at::TensorOptions().dtype(at::kFloat).device(at::kCUDA, device));
+}
+
+void tp_p2p_allreduce_rmsnorm(const Tensor& x_in, const Tensor& x_out, const Tensor& parts, int64_t flags_local,
+                              const Tensor& flag_ptrs, int64_t n, int64_t me, const Tensor& epoch,
+                              const c10::optional<Tensor>& w, double eps, const c10::optional<Tensor>& xq,
+                              const c10::optional<Tensor>& xd, const c10::optional<Tensor>& xs,
+                              const c10::optional<Tensor>& yb, const Tensor& status, bool pdl, int64_t wait_ns) {
+  TORCH_CHECK(x_in.is_cuda() && x_in.scalar_type() == at::kFloat && x_out.scalar_type() == at::kFloat &&
+                  x_in.stride(0) == x_out.stride(0),
+              "tp p2p norm: fp32 residual rows with equal strides");
+  TORCH_CHECK(parts.scalar_type() == at::kLong && parts.numel() == n && flag_ptrs.scalar_type() == at::kLong &&
+                  flag_ptrs.numel() == n,
+              "tp p2p norm: int64 address tables of n ranks");
+  hk::TpP2PArgs a{};
+  a.x_in = x_in.data_ptr<float>();
+  a.x_out = x_out.data_ptr<float>();
+  a.x_stride = x_in.stride(0);
+  a.parts = reinterpret_cast<const unsigned long long*>(parts.data_ptr<int64_t>());
+  a.flags_local = as_ptr<unsigned int>(flags_local);
+  a.flag_ptrs = reinterpret_cast<const unsigned long long*>(flag_ptrs.data_ptr<int64_t>());
+  a.n = (int)n;
+  a.me = (int)me;
+  a.epoch = epoch.data_ptr<int>();
+  a.w = w.has_value() ? w->data_ptr<float>() : nullptr;
+  a.eps = (float)eps;
+  a.K = (int)x_in.size(1);
+  if (xq.has_value()) {
+    TORCH_CHECK(xd.has_value() && xs.has_value(), "tp p2p norm: q8 output needs q, d and s");
+    a.xq = xq->data_ptr<int8_t>();
+    a.xd = xd->data_ptr<float>();
+    a.xs = xs->data_ptr<float>();
+  } else {
+    TORCH_CHECK(yb.has_value() && yb->scalar_type() == at::kBFloat16 && yb->stride(-1) == 1,
+                "tp p2p norm: a q8 or a bf16 output is required");
+    a.yb = reinterpret_cast<__nv_bfloat16*>(yb->data_ptr());
+    a.yb_stride = yb->stride(0);
+  }
+  a.status = status.data_ptr<int>();
+  a.wait_ns = (unsigned long long)(wait_ns > 0 ? wait_ns : 0);
+  const c10::cuda::CUDAGuard g(x_in.device());
+  hk::tp_p2p_allreduce_rmsnorm_launch(a, (int)x_in.size(0), cur_stream(), pdl);
+}
+
 void register_tp_kernels(py::module_& m) {
+  m.def("wrap_f32", &wrap_f32, py::arg("ptr"), py::arg("numel"), py::arg("device"));
+  m.def("tp_p2p_allreduce_rmsnorm", &tp_p2p_allreduce_rmsnorm, py::arg("x_in"), py::arg("x_out"), py::arg("parts"),
+        py::arg("flags_local"), py::arg("flag_ptrs"), py::arg("n"), py::arg("me"), py::arg("epoch"), py::arg("w"),
+        py::arg("eps"), py::arg("xq") = py::none(), py::arg("xd") = py::none(), py::arg("xs") = py::none(),
+        py::arg("yb") = py::none(), py::arg("status"), py::arg("pdl") = false, py::arg("wait_ns") = 0);
   m.def("ipc_malloc", &ipc_malloc, py::arg("bytes"));
   m.def("ipc_handle", &ipc_handle, py::arg("ptr"));
   m.def("ipc_open", &ipc_open, py::arg("handle"));

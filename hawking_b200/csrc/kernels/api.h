@@ -91,6 +91,31 @@ struct TpReduceArgs {
   int* status;
   unsigned long long wait_ns;   // bound of each peer wait (0: the default, one second)
 };
+// Tensor-core path (up to wide_rows rows): every rank's row-parallel GEMM accumulates its partial
+// into its own IPC-shared buffer of the site; this consumer raises the rank's flag of the site on
+// every peer, waits (bounded) for all N flags, reads the N partials over NVLink (P2P loads, fixed
+// rank order), adds the residual and normalises, as tp_allreduce_rmsnorm does for pushed words.
+struct TpP2PArgs {
+  const float* x_in;
+  float* x_out;
+  int64_t x_stride;
+  const unsigned long long* parts;      // [n] addresses of every rank's partial of the site [rows][K]
+  unsigned int* flags_local;            // this rank's flags of the site [n] (peers write slot `src`)
+  const unsigned long long* flag_ptrs;  // [n] addresses of every rank's flags of the site
+  int n, me;
+  const int* epoch;                     // flag value of this forward
+  const float* w;
+  float eps;
+  int K;
+  int8_t* xq;
+  float* xd;
+  float* xs;
+  __nv_bfloat16* yb;
+  int64_t yb_stride;
+  int* status;
+  unsigned long long wait_ns;
+};
+void tp_p2p_allreduce_rmsnorm_launch(const TpP2PArgs& a, int rows, cudaStream_t s, bool pdl);
 struct TpArgmaxArgs {
   unsigned long long* slots;    // local fused-argmax slots [rows, kArgmaxSlots] (cleared here)
   int rows, max_rows;

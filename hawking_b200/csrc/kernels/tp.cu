@@ -139,6 +139,113 @@ void tp_allreduce_rmsnorm_q8_launch(const TpReduceArgs& a, int rows, cudaStream_
   launch(tp_allreduce_rmsnorm_q8_kernel, dim3(kTpCluster, rows), dim3(256), 0, s, pdl, a);
 }
 
+// ---- tensor-core path: P2P-read all-reduce + RMSNorm ----------------------------------------------
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Grid (kTpCluster, rows) as the push consumer. Every CTA's thread 0 raises this rank's flag of the
+// site on every rank (the GEMM that wrote the partial completed before this kernel: the dependency
+// wait), threads 0..n-1 wait for the n flags, then the CTA reads its elements of the n partials
+// (remote ones over NVLink, uncached loads) in rank order.
+__global__ void __cluster_dims__(kTpCluster, 1, 1) __launch_bounds__(256)
+    tp_p2p_allreduce_rmsnorm_kernel(TpP2PArgs a) {
+  __shared__ float red[8];
+  __shared__ float part_ss;
+  pdl_wait();
+  cg::cluster_group cluster = cg::this_cluster();
+  const int c = (int)cluster.block_rank();
+  const int r = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int K = a.K, chunk = K / kTpCluster, base = c * chunk, n = a.n;
+  const unsigned flag = (unsigned)*a.epoch;
+  if (tid == 0) {
+    __threadfence_system();
+    for (int p = 0; p < n; ++p) st_release_sys(reinterpret_cast<unsigned*>(a.flag_ptrs[p]) + a.me, flag);
+  }
+  bool ok = true;
+  if (tid < n) {
+    const unsigned long long deadline = global_ns() + (a.wait_ns ? a.wait_ns : kTpWaitNs);
+    while (ld_acquire_sys(a.flags_local + tid) != flag) {
+      if (global_ns() > deadline) {
+        ok = false;
+        break;
+      }
+    }
+  }
+  ok = __syncthreads_and(ok);
+  if (!ok && tid == 0) set_error(a.status, HK_ERR_PEER_TIMEOUT);
+  const float* xr = a.x_in + (int64_t)r * a.x_stride;
+  float v[kTpMaxE];
+#pragma unroll
+  for (int j = 0; j < kTpMaxE; ++j) {
+    const bool on = j * 256 + warp * 32 < chunk;
+    v[j] = on ? xr[base + j * 256 + tid] : 0.f;
+  }
+  for (int p = 0; p < n; ++p) {  // fixed rank order: the same sum on every rank
+    const float* pr = reinterpret_cast<const float*>(a.parts[p]) + (int64_t)r * K;
+    float t[kTpMaxE];
+#pragma unroll
+    for (int j = 0; j < kTpMaxE; ++j) {
+      const bool on = j * 256 + warp * 32 < chunk;
+      t[j] = on ? __ldcv(pr + base + j * 256 + tid) : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < kTpMaxE; ++j) v[j] += t[j];
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < kTpMaxE; ++j) ss += v[j] * v[j];
+  ss = warp_sum(ss);
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  if (tid == 0) {
+    float tt = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) tt += red[i];
+    part_ss = tt;
+  }
+  cluster.sync();
+  float total = 0.f;
+#pragma unroll
+  for (int i = 0; i < kTpCluster; ++i) total += *cluster.map_shared_rank(&part_ss, i);
+  cluster.sync();
+  const float scale = rsqrtf(total / K + a.eps);
+  pdl_launch();
+#pragma unroll
+  for (int j = 0; j < kTpMaxE; ++j) {
+    if (j * 256 + warp * 32 >= chunk) continue;  // warp-uniform
+    const int e = base + j * 256 + tid;
+    a.x_out[(int64_t)r * a.x_stride + e] = v[j];
+    float y = v[j] * scale;
+    if (a.w) y *= a.w[e];
+    if (!a.xq) {
+      if (a.yb) a.yb[(int64_t)r * a.yb_stride + e] = __float2bfloat16_rn(y);
+      continue;
+    }
+    const float amax = warp_max(fabsf(y));
+    const float d = amax / 127.f;
+    const int q = amax > 0.f ? __float2int_rn(y / d) : 0;
+    const float qsum = warp_sum((float)q);
+    a.xq[(int64_t)r * K + e] = (int8_t)q;
+    if (lane == 0) {
+      a.xd[(int64_t)r * (K / 32) + (e >> 5)] = d;
+      a.xs[(int64_t)r * (K / 32) + (e >> 5)] = d * qsum;
+    }
+  }
+}
+
+void tp_p2p_allreduce_rmsnorm_launch(const TpP2PArgs& a, int rows, cudaStream_t s, bool pdl) {
+  if (a.K % (32 * kTpCluster) || a.K > kTpCluster * 256 * kTpMaxE || a.x_stride % 4)
+    throw std::runtime_error("tp p2p all-reduce norm: K must be a multiple of 256 and at most 8192");
+  if (a.n < 1 || a.n > kTpMaxRanks || a.me < 0 || a.me >= a.n) throw std::runtime_error("tp p2p all-reduce norm: 1..8 ranks");
+  launch(tp_p2p_allreduce_rmsnorm_kernel, dim3(kTpCluster, rows), dim3(256), 0, s, pdl, a);
+}
+
 // Vocabulary-parallel greedy: local best packed key per row (from the fused LM-head slots,
 // already holding global indices) -> pushed to every rank -> max of the N keys -> token id.
 __global__ void __launch_bounds__(256) tp_argmax_kernel(TpArgmaxArgs a) {

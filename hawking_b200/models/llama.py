@@ -366,8 +366,10 @@ class LlamaModel:
         x = self.x[:rows]
         tc = self.use_tensor_cores(rows)
         tp = self.tp
-        if tp is not None and not tc:
-            ops.tp_begin(tp)  # one epoch per forward that uses the push all-reduce sites
+        # tensor-core forwards of up to tp.wide_rows rows all-reduce through the P2P-read sites
+        wide = tp is not None and tc and 0 < rows <= getattr(tp, "wide_rows", 0)
+        if tp is not None and (not tc or wide):
+            ops.tp_begin(tp)  # one epoch per forward that uses the push / P2P all-reduce sites
         ops.embed(w.embed, inp.ids[:rows], x)
         if self.dstep is not None and tp is None and not tc and n_logits == 0 and not self.long_runs \
                 and self.small_batch == "w4a16" and self.dstep.supports(rows):
@@ -387,8 +389,8 @@ class LlamaModel:
                 self._layer_gemv_tp(l, lw, rows, splits)
                 continue
             if tc:
-                self._attention_block_tc(l, lw, rows, splits)
-                self._ffn_block_tc(lw, rows)
+                self._attention_block_tc(l, lw, rows, splits, wide)
+                self._ffn_block_tc(lw, rows, l, wide)
             elif self._mg_layer(lw):
                 self._layer_mg(l, lw, rows, splits)
             else:
@@ -676,9 +678,12 @@ class LlamaModel:
             self._tp_full = torch.zeros(self.max_logit_rows, V, device=self.dev)
         return self._tp_full[:nl]
 
-    def _attention_block_tc(self, l, lw, rows, splits):
+    def _attention_block_tc(self, l, lw, rows, splits, wide: bool = False):
+        """``wide``: tensor parallel over the P2P-read sites; the previous layer's site already
+        left norm(x) in self.xb, and this layer's O site writes the residual into self.x2."""
         x = self.x[:rows]
-        ops.rmsnorm(x, lw.attn_norm, self.cfg.eps, yb=self.xb[:rows])
+        if not (wide and l > 0):
+            ops.rmsnorm(x, lw.attn_norm, self.cfg.eps, yb=self.xb[:rows])
         qkv = self.qkv[:rows]
         once = ops.tc_gemm_overwrites(rows)  # persistent GEMM: plain stores, nothing to zero
         if not once:
@@ -688,7 +693,12 @@ class LlamaModel:
             ops.tc_gemm(wt, self.xb[:rows], qkv[:, off:off + wt.N], self.status, y_zeroed=not once)
             off += wt.N
         self._rope_attention(l, lw, rows, splits, out_bf16=self.attb[:rows])
-        if self.tp is not None:
+        if wide:
+            part = self.tp.wide_part(2 * l)[:rows]
+            self._tc_partial(lw.wo, self.attb[:rows], part, once)
+            ops.tp_p2p_allreduce_rmsnorm(self.tp, 2 * l, x, self.x2[:rows], lw.ffn_norm, self.cfg.eps,
+                                         out_bf16=self.xb[:rows])
+        elif self.tp is not None:
             if once:
                 ops.tc_gemm(lw.wo, self.attb[:rows], self.partial[:rows], self.status)
             else:
@@ -698,10 +708,20 @@ class LlamaModel:
         else:
             ops.tc_gemm(lw.wo, self.attb[:rows], x, self.status, atomic=True)
 
-    def _ffn_block_tc(self, lw, rows):
-        x = self.x[:rows]
+    def _tc_partial(self, wt, src, out, once: bool):
+        """This rank's partial of a row-parallel projection into ``out`` (plain stores from the
+        persistent GEMM, else split-K accumulation into a zeroed buffer)."""
+        if once:
+            ops.tc_gemm(wt, src, out, self.status)
+        else:
+            out.zero_()
+            ops.tc_gemm(wt, src, out, self.status, atomic=True, y_zeroed=True)
+
+    def _ffn_block_tc(self, lw, rows, l: int = 0, wide: bool = False):
+        x = self.x2[:rows] if wide else self.x[:rows]
         F = lw.w_down.K
-        ops.rmsnorm(x, lw.ffn_norm, self.cfg.eps, yb=self.xb[:rows])
+        if not wide:  # wide: the O site left norm(x2) in self.xb
+            ops.rmsnorm(x, lw.ffn_norm, self.cfg.eps, yb=self.xb[:rows])
         bn = 64 if rows <= 64 else (128 if rows < 192 else 256)
         if self.fuse_swiglu_tc and F % 64 == 0 and lw.w_gu.N == 2 * F and (F // 64) * -(-rows // bn) >= 148:
             # SwiGLU in the GEMM epilogue (enough tiles to fill the GPU without split-K)
@@ -710,7 +730,14 @@ class LlamaModel:
             gu = self.gu[:rows, : 2 * F]
             ops.tc_gemm(lw.w_gu, self.xb[:rows], gu, self.status, y_zeroed=True)
             ops.swiglu_bf16(gu, F, self.hb[:rows, :F], clear=True)
-        if self.tp is not None:
+        if wide:
+            part = self.tp.wide_part(2 * l + 1)[:rows]
+            self._tc_partial(lw.w_down, self.hb[:rows, :F], part, ops.tc_gemm_overwrites(rows))
+            layers = self.w.layers
+            nxt = layers[l + 1].attn_norm if l + 1 < len(layers) else self.w.out_norm
+            ops.tp_p2p_allreduce_rmsnorm(self.tp, 2 * l + 1, x, self.x[:rows], nxt, self.cfg.eps,
+                                         out_bf16=self.xb[:rows])
+        elif self.tp is not None:
             if ops.tc_gemm_overwrites(rows):
                 ops.tc_gemm(lw.w_down, self.hb[:rows, :F], self.partial[:rows], self.status)
             else:

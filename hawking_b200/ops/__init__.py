@@ -176,6 +176,18 @@ def rope_append(qkv, positions, slots, rope, rot_dim, style, q_out, k_cache, v_c
                           v_cache, nh, nkv, hd, block_size, block_tables, row_seq, PDL)
 
 
+def tp_p2p_allreduce_rmsnorm(tp, site: int, x_in, x_out, w, eps: float, out=None, out_bf16=None):
+    """Tensor-core path all-reduce of a row-parallel site (the rank's GEMM accumulated into
+    ``tp.wide_part(site)``): flags raised on every rank, the N partials read over NVLink in rank
+    order, x_out = x_in + their sum, RMSNorm (weight ``w``) into q8 blocks or bf16 rows."""
+    launches.add()
+    kernels().tp_p2p_allreduce_rmsnorm(
+        x_in, x_out, tp.wide_parts[site], tp.wide_flags_local(site), tp.wide_flag_ptrs[site], tp.world, tp.rank,
+        tp.epoch, w, eps, xq=out.q if out is not None else None, xd=out.d if out is not None else None,
+        xs=out.s if out is not None else None, yb=out_bf16, status=tp.status, pdl=PDL,
+        wait_ns=getattr(tp, "wait_ns", 0))
+
+
 def advance(ids, next_ids, positions, row_ctx, rows: int):
     launches.add()
     kernels().advance(ids, next_ids, positions, row_ctx, rows, PDL)

@@ -135,7 +135,7 @@ class TPComm:
     """Shared buffers and pointer tables of the fused collectives for one rank."""
 
     def __init__(self, rank: int, world: int, n_sites: int, max_rows: int, width: int, device,
-                 group: Optional[dist.ProcessGroup] = None, key_rows: int = 64):
+                 group: Optional[dist.ProcessGroup] = None, key_rows: int = 64, wide_rows: int = 64):
         """``max_rows``: rows of the push all-reduce (GEMV path); ``key_rows``: rows of the greedy
         key exchange (any decode batch)."""
         K = kernels()
@@ -174,7 +174,40 @@ class TPComm:
         self.push_recv = [table([self.ptrs[p] + 8 * (s * self.site_words + rank * self.rank_stride)
                                  for p in range(world)]) for s in range(n_sites)]
         self.keys_table = table([self.ptrs[p] + self.keys_off for p in range(world)])
+        # tensor-core path sites (up to wide_rows rows): per site an fp32 partial [wide_rows, width]
+        # that the rank's GEMM accumulates into, read by every rank over NVLink, and per site the
+        # ranks' ready flags [world] (uint32, written by the peers)
+        self.wide_rows = wide_rows if world > 1 else 0
+        self.wide_base, self.wide_ptrs = 0, []
+        if self.wide_rows:
+            part_bytes = n_sites * wide_rows * width * 4
+            self.wide_flags_off = part_bytes
+            wtotal = (part_bytes + n_sites * world * 4 + 255) // 256 * 256
+            with torch.cuda.device(self.dev):
+                self.wide_base = K.ipc_malloc(wtotal)
+                torch.cuda.synchronize(self.dev)
+                K.wrap_f32(self.wide_base, wtotal // 4, self.dev.index or 0).zero_()
+                torch.cuda.synchronize(self.dev)
+                wh = bytes(K.ipc_handle(self.wide_base))
+            whs = [None] * world
+            dist.all_gather_object(whs, wh, group=group)
+            with torch.cuda.device(self.dev):
+                self.wide_ptrs = [self.wide_base if p == rank else K.ipc_open(h) for p, h in enumerate(whs)]
+            site_floats = wide_rows * width
+            self.wide_parts = [table([self.wide_ptrs[p] + 4 * s * site_floats for p in range(world)])
+                               for s in range(n_sites)]
+            self.wide_flag_ptrs = [table([self.wide_ptrs[p] + self.wide_flags_off + 4 * s * world
+                                          for p in range(world)]) for s in range(n_sites)]
+            self._wide_local = K.wrap_f32(self.wide_base, n_sites * site_floats, self.dev.index or 0).view(
+                n_sites, wide_rows, width)
         self.closed = False
+
+    def wide_part(self, site: int) -> torch.Tensor:
+        """This rank's partial buffer of a tensor-core site, [wide_rows, width] fp32."""
+        return self._wide_local[site]
+
+    def wide_flags_local(self, site: int) -> int:
+        return self.wide_base + self.wide_flags_off + 4 * site * self.world
 
     # local addresses
     def recv_local(self, site: int) -> int:
@@ -200,10 +233,16 @@ class TPComm:
             for p, ptr in enumerate(self.ptrs):
                 if p != self.rank:
                     K.ipc_close(ptr)
+            for p, ptr in enumerate(self.wide_ptrs):
+                if p != self.rank:
+                    K.ipc_close(ptr)
         if self.world > 1:
             dist.barrier(group=self.group)
         with torch.cuda.device(self.dev):
             K.ipc_free(self.base)
+            if self.wide_base:
+                self._wide_local = None
+                K.ipc_free(self.wide_base)
         self.closed = True
 
 

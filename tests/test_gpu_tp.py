@@ -246,3 +246,68 @@ def test_tp2_sampling_matches_tp1(tmp_path):
     assert r["gens"][0] == r["gens"][1], r  # every rank draws the same tokens
     assert r["gens"][0] == r["ref_gen"], r  # and the one-GPU engine draws them too (same seed)
     assert r["ref_gen"] != r["greedy"], r  # it really sampled
+
+
+def _tc_wide_worker(rank, world, port, out_path):
+    """Tensor-core path at up to 64 rows: row-parallel GEMM partials all-reduced by the P2P-read
+    consumer (no NCCL), against one GPU on the same path."""
+    import datetime
+
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        from hawking_b200.engine.engine import Engine
+        from hawking_b200.engine.sampling import SamplingParams
+        from hawking_b200.models.config import preset
+        from hawking_b200.models.llama import random_llama_weights
+        from hawking_b200.parallel.tp import TPComm, local_config, shard_llama_weights
+        cfg = preset("llama3-8b", layers=2, hidden=1024, n_heads=8, n_kv_heads=2, ffn=2048, vocab=2048, max_ctx=128)
+        w = random_llama_weights(cfg, dev, seed=7, std=0.05)
+        tp = TPComm(rank, world, 2 * cfg.layers, 8, cfg.hidden, dev)
+        eng = Engine.build(local_config(cfg, world), shard_llama_weights(w, cfg, rank, world), device=dev,
+                           max_batch=4, max_ctx=128, block_size=16, num_blocks=64, max_rows=64, tp=tp)
+        eng.model.tc_min_rows = 1  # the tensor-core path at every row count
+        toks = list(range(10, 34))  # 24 rows: one tensor-core forward through the P2P sites
+        local = eng.model.forward_tokens(toks, seq_id=1)
+        eng.kv.drop(1)
+        parts = [torch.empty_like(local) for _ in range(world)]
+        dist.all_gather(parts, local.contiguous())
+        full = torch.cat(parts, 1)
+        gen = eng.generate([list(range(30, 40)), list(range(50, 53)), list(range(60, 70))],
+                           SamplingParams(max_tokens=6))
+        gens = [None] * world
+        dist.all_gather_object(gens, gen)
+        tp.check()
+        if rank == 0:
+            ref = Engine.build(cfg, w, device=dev, max_batch=4, max_ctx=128, block_size=16, num_blocks=64,
+                               max_rows=64)
+            ref.model.tc_min_rows = 1
+            ref_logits = ref.model.forward_tokens(toks, seq_id=1)
+            ref.kv.drop(1)
+            ref_gen = ref.generate([list(range(30, 40)), list(range(50, 53)), list(range(60, 70))],
+                                   SamplingParams(max_tokens=6))
+            err = float((full - ref_logits).abs().max() / ref_logits.abs().max())
+            torch.save({"err": err, "gens": gens, "ref_gen": ref_gen}, out_path)
+        torch.cuda.synchronize()
+        eng.model.release_graphs()
+        tp.close()
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp2_tensor_core_p2p_allreduce_matches_tp1(tmp_path):
+    import torch.multiprocessing as mp
+    out = str(tmp_path / "tcwide.pt")
+    mp.spawn(_tc_wide_worker, args=(2, _free_port(), out), nprocs=2, join=True)
+    r = torch.load(out)
+    assert r["err"] < 0.01, r
+    assert r["gens"][0] == r["gens"][1], r
+    assert [g[0] for g in r["gens"][0]] == [g[0] for g in r["ref_gen"]], r
