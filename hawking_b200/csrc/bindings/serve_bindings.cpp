@@ -33,6 +33,11 @@ void bind_serve(py::module_& m) {
       .def_static("from_spec", [](const TokenizerSpec& s) { return std::shared_ptr<Tokenizer>(Tokenizer::from_spec(s)); })
       .def_static("from_gguf",
                   [](const GgufFile& f) { return std::shared_ptr<Tokenizer>(Tokenizer::from_gguf(f)); })
+      .def_static("from_json",
+                  [](const std::string& path, const std::string& config) {
+                    return std::shared_ptr<Tokenizer>(Tokenizer::from_json(path, config));
+                  },
+                  py::arg("path"), py::arg("config") = "")
       .def("encode", &Tokenizer::encode, py::arg("text"), py::arg("add_special") = true,
            py::call_guard<py::gil_scoped_release>())
       .def("decode", &Tokenizer::decode, py::arg("ids"), py::arg("skip_special") = true)

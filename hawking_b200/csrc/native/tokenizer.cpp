@@ -1,6 +1,10 @@
 // GGUF-vocabulary tokenizer; see tokenizer.h.
 #include "tokenizer.h"
 
+#include <cstdio>
+
+#include "json.h"
+
 #include <algorithm>
 #include <climits>
 #include <cstdint>
@@ -304,6 +308,143 @@ std::unique_ptr<Tokenizer> Tokenizer::from_gguf(const GgufFile& f) {
   if (it != kv.end()) sp.add_bos = it->second.i != 0;
   it = kv.find("tokenizer.ggml.add_eos_token");
   if (it != kv.end()) sp.add_eos = it->second.i != 0;
+  return from_spec(sp);
+}
+
+namespace {
+// The pre-tokenizer rule set named by a Split regex of a tokenizer.json.
+std::string pre_from_regex(const std::string& re) {
+  const bool three_digits = re.find("\\p{N}{1,3}") != std::string::npos;
+  const bool single_digit = re.find("|\\p{N}|") != std::string::npos || re.find("\\p{N}|") != std::string::npos;
+  const bool ci_contractions = re.find("(?i:'s|'t|'re|'ve|'m|'ll|'d)") != std::string::npos;
+  if (three_digits && ci_contractions) return "llama-bpe";
+  if (ci_contractions && single_digit) return "qwen2";
+  return "default";
+}
+void find_split_regex(const Json& pt, std::string* re, bool* byte_level) {
+  if (!pt.is_object()) return;
+  const std::string type = pt.has("type") ? pt["type"].as_string() : "";
+  if (type == "ByteLevel") *byte_level = true;
+  if (type == "Split" && pt.has("pattern") && pt["pattern"].is_object()) {
+    const Json& pat = pt["pattern"];
+    if (pat.has("Regex")) *re = pat["Regex"].as_string();
+  }
+  if (type == "Sequence" && pt.has("pretokenizers"))
+    for (const auto& sub : pt["pretokenizers"].items()) find_split_regex(sub, re, byte_level);
+}
+std::string read_file(const std::string& path) {
+  FILE* f = std::fopen(path.c_str(), "rb");
+  if (!f) throw std::runtime_error("tokenizer: cannot open " + path);
+  std::string s;
+  char buf[1 << 16];
+  size_t n;
+  while ((n = std::fread(buf, 1, sizeof buf, f)) > 0) s.append(buf, n);
+  std::fclose(f);
+  return s;
+}
+std::string token_text(const Json& v) {  // "bos_token": "<s>" or {"content": "<s>", ...}
+  if (v.is_string()) return v.as_string();
+  if (v.is_object() && v.has("content")) return v["content"].as_string();
+  return "";
+}
+}  // namespace
+
+std::unique_ptr<Tokenizer> Tokenizer::from_json(const std::string& tokenizer_json, const std::string& config_json) {
+  const Json j = Json::parse(read_file(tokenizer_json));
+  const Json& model = j["model"];
+  if (!model.is_object()) throw std::runtime_error("tokenizer.json: no model");
+  const std::string type = model.has("type") ? model["type"].as_string() : "BPE";
+  TokenizerSpec sp;
+  std::vector<std::string> tokens;
+  std::vector<float> scores;
+  auto put = [&](int64_t id, const std::string& s, float score) {
+    if (id < 0) throw std::runtime_error("tokenizer.json: negative id");
+    if ((size_t)id >= tokens.size()) {
+      tokens.resize((size_t)id + 1);
+      scores.resize((size_t)id + 1, -1e9f);
+    }
+    tokens[(size_t)id] = s;
+    scores[(size_t)id] = score;
+  };
+  std::unordered_map<std::string, int64_t> rank_of;  // merged token -> merge rank (byte fallback)
+  if (type == "BPE") {
+    for (const auto& kv : model["vocab"].members()) put(kv.second.as_int(), kv.first, 0.f);
+    const Json& merges = model["merges"];
+    int64_t r = 0;
+    for (const auto& m : merges.items()) {
+      std::string a, b;
+      if (m.is_string()) {
+        const std::string& t = m.as_string();
+        const size_t sp_pos = t.find(' ');
+        if (sp_pos == std::string::npos) continue;
+        a = t.substr(0, sp_pos);
+        b = t.substr(sp_pos + 1);
+      } else if (m.is_array() && m.size() == 2) {
+        a = m.at(0).as_string();
+        b = m.at(1).as_string();
+      } else {
+        continue;
+      }
+      sp.merges.push_back(a + " " + b);
+      rank_of.emplace(a + b, r++);
+    }
+  } else if (type == "Unigram") {
+    int64_t id = 0;
+    for (const auto& e : model["vocab"].items()) put(id++, e.at(0).as_string(), (float)e.at(1).as_double());
+    if (model.has("unk_id") && model["unk_id"].is_number()) sp.unk = (int32_t)model["unk_id"].as_int();
+  } else {
+    throw std::runtime_error("tokenizer.json: model type '" + type + "' not supported");
+  }
+  std::vector<int32_t> types;
+  if (j.has("added_tokens"))
+    for (const auto& t : j["added_tokens"].items()) {
+      const int64_t id = t["id"].as_int();
+      put(id, t["content"].as_string(), 0.f);
+      if (types.size() < tokens.size()) types.resize(tokens.size(), 1);
+      types[(size_t)id] = t.has("special") && t["special"].as_bool() ? 3 : 4;
+    }
+  types.resize(tokens.size(), 1);
+  for (size_t i = 0; i < tokens.size(); ++i)
+    if (tokens[i].empty()) {
+      tokens[i] = "[UNUSED_" + std::to_string(i) + "]";
+      types[i] = 3;
+    }
+  const bool byte_fallback = type == "BPE" && model.has("byte_fallback") && model["byte_fallback"].as_bool();
+  if (type == "Unigram" || byte_fallback) {
+    // SentencePiece: highest score merges first; a BPE vocabulary's merge order becomes the score
+    sp.model = "llama";
+    if (byte_fallback) {
+      for (size_t i = 0; i < tokens.size(); ++i) {
+        auto it = rank_of.find(tokens[i]);
+        scores[i] = it == rank_of.end() ? -1e9f : -(float)it->second;
+      }
+      sp.merges.clear();
+    }
+    sp.scores = scores;
+  } else {
+    sp.model = "gpt2";
+    std::string re;
+    bool byte_level = false;
+    find_split_regex(j["pre_tokenizer"], &re, &byte_level);
+    if (!byte_level) throw std::runtime_error("tokenizer.json: BPE without a ByteLevel pre-tokenizer");
+    sp.pre = re.empty() ? "default" : pre_from_regex(re);
+  }
+  sp.tokens = tokens;
+  sp.token_types = types;
+  auto id_of = [&](const std::string& s) -> int32_t {
+    for (size_t i = 0; i < tokens.size(); ++i)
+      if (tokens[i] == s) return (int32_t)i;
+    return -1;
+  };
+  if (!config_json.empty()) {
+    const Json c = Json::parse(read_file(config_json));
+    if (c.has("bos_token")) sp.bos = id_of(token_text(c["bos_token"]));
+    if (c.has("eos_token")) sp.eos = id_of(token_text(c["eos_token"]));
+    if (c.has("unk_token")) sp.unk = id_of(token_text(c["unk_token"]));
+    if (c.has("pad_token")) sp.pad = id_of(token_text(c["pad_token"]));
+    if (c.has("add_bos_token") && !c["add_bos_token"].is_null()) sp.add_bos = c["add_bos_token"].as_bool() ? 1 : 0;
+    if (c.has("add_eos_token") && !c["add_eos_token"].is_null()) sp.add_eos = c["add_eos_token"].as_bool();
+  }
   return from_spec(sp);
 }
 

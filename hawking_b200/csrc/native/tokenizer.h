@@ -1,4 +1,4 @@
-// Tokenizer built from the vocabulary embedded in a GGUF file (no tokenizer.json needed).
+// Tokenizer built from the vocabulary embedded in a GGUF file, or from a Hugging Face tokenizer.json.
 //
 // Two GGUF vocabulary kinds are supported:
 //   * byte-level BPE (`tokenizer.ggml.model` = "gpt2", or "llama" with merges): text is split
@@ -13,7 +13,8 @@
 //
 // Parity: crates/hawking-core/src/tokenizer.rs:156 (from_gguf), :241 (encode), :266 (decode),
 // :281 (decode_one), :309 (is_eog), :68-115 (special / end-of-generation sets), :362
-// (add_bos default for "llama-bpe"), :417-548 (SentencePiece bigram merge with byte fallback).
+// (add_bos default for "llama-bpe"), :417-548 (SentencePiece bigram merge with byte fallback), :131
+// (Tokenizer::from_file, tokenizer.json).
 #pragma once
 #include <cstdint>
 #include <memory>
@@ -42,6 +43,12 @@ class Tokenizer {
  public:
   static std::unique_ptr<Tokenizer> from_spec(const TokenizerSpec& spec);
   static std::unique_ptr<Tokenizer> from_gguf(const GgufFile& f);
+  // Hugging Face `tokenizer.json` (+ the `tokenizer_config.json` beside it, when present, for the
+  // bos / eos tokens and add_bos): model BPE with a ByteLevel pre-tokenizer (its split regex
+  // mapped to the GPT-2 / Llama-3 / Qwen2 rules), BPE with byte fallback (SentencePiece-style:
+  // merge ranks become scores), or Unigram (SentencePiece with its scores). Added tokens are
+  // control tokens when marked special.
+  static std::unique_ptr<Tokenizer> from_json(const std::string& tokenizer_json, const std::string& config_json = "");
 
   std::vector<int32_t> encode(const std::string& text, bool add_special = true) const;
   std::string decode(const std::vector<int32_t>& ids, bool skip_special = true) const;

@@ -23,7 +23,8 @@ def main(argv=None):
     ap.add_argument("--model", default=None, help="a GGUF file or a .gravity artifact (container sniffed)")
     ap.add_argument("--preset", default=None, help="serve random-init weights of this architecture preset")
     ap.add_argument("--layers", type=int, default=0, help="with --preset: override the layer count")
-    ap.add_argument("--tokenizer-gguf", default=None, help="with --preset: the tokenizer (default: synthetic)")
+    ap.add_argument("--tokenizer-gguf", default=None,
+                    help="with --preset / --model: the tokenizer, a GGUF or a tokenizer.json (default: synthetic)")
     ap.add_argument("--host", default="127.0.0.1")
     ap.add_argument("--port", type=int, default=8000)
     ap.add_argument("--model-id", default=None)
@@ -144,7 +145,16 @@ def path_engine(path: str, max_batch: int = 8, max_ctx=None, tokenizer_gguf=None
         else:
             tp = os.path.join(tempfile.mkdtemp(prefix="hk-tok-"), "tokenizer.gguf")
             write_tokenizer_gguf(tp, eng.cfg.vocab)
-    return eng, native().Tokenizer.from_gguf(native().GgufFile.open(tp))
+    return eng, load_tokenizer(tp)
+
+
+def load_tokenizer(path: str):
+    """A GGUF file's embedded vocabulary, or a Hugging Face tokenizer.json (with the
+    tokenizer_config.json beside it when present)."""
+    if path.endswith(".json"):
+        cfg = os.path.join(os.path.dirname(os.path.abspath(path)), "tokenizer_config.json")
+        return native().Tokenizer.from_json(path, cfg if os.path.exists(cfg) else "")
+    return native().Tokenizer.from_gguf(native().GgufFile.open(path))
 
 
 def preset_engine(preset: str, layers: int = 0, max_batch: int = 8, max_ctx=None, tokenizer_gguf=None,
@@ -195,8 +205,7 @@ def preset_engine(preset: str, layers: int = 0, max_batch: int = 8, max_ctx=None
     if path is None:
         path = os.path.join(tempfile.mkdtemp(prefix="hk-tok-"), "tokenizer.gguf")
         write_tokenizer_gguf(path, cfg.vocab)
-    tok = native().Tokenizer.from_gguf(native().GgufFile.open(path))
-    return eng, tok
+    return eng, load_tokenizer(path)
 
 
 if __name__ == "__main__":
