@@ -77,6 +77,7 @@ class Engine:
         self.sched = native().Scheduler(kv.bm, max_batch, max_prefill_tokens, policy)
         self.requests: Dict[int, RequestState] = {}
         self._ids = itertools.count(1)
+        self._keep: Optional[List[int]] = None  # pruned LM head: original id of every kept row
         self.use_graphs = use_graphs
         self.stats = EngineStats()
         self._host_ids = torch.zeros(model.max_rows, dtype=torch.int32).pin_memory()
@@ -191,9 +192,11 @@ class Engine:
 
     @staticmethod
     def from_gguf(path: str, device="cuda", max_batch: int = 8, max_ctx: Optional[int] = None,
-                  tp_rank: int = 0, tp_world: int = 1, **kw):
+                  tp_rank: int = 0, tp_world: int = 1, quant_tier_map: Optional[str] = None, **kw):
         """Load a GGUF model (weights re-laid for the kernels) and build an engine around it.
-        ``tp_world > 1``: this rank's tensor-parallel shard (the process group must be up)."""
+        ``tp_world > 1``: this rank's tensor-parallel shard (the process group must be up).
+        ``quant_tier_map``: JSON of per-layer FFN formats; those weights are re-quantised on the
+        device before the kernels' re-lay (engine/vocab_prune.py QuantTierMap)."""
         from ..formats.gguf import GgufModel
         from ..models.llama import load_llama_weights
         from ..models.torch_ref import config_from_gguf
@@ -211,6 +214,9 @@ class Engine:
         check_memory_budget(sum(ti.nbytes for ti in m.tensors.values()), free, f"weights of {path}")
         t = time.perf_counter()
         w = load_llama_weights(m, cfg, device)
+        if quant_tier_map:
+            from .vocab_prune import QuantTierMap
+            QuantTierMap.load(quant_tier_map).apply(w, cfg)
         torch.cuda.synchronize(device)
         ph["weights"] = (time.perf_counter() - t) * 1e3
         t = time.perf_counter()
@@ -282,8 +288,19 @@ class Engine:
                 self.stats_disk["stored"] += 1
 
     # ---- requests ----
+    def enable_vocab_prune(self, pv):
+        """Prune the model's LM head to the whitelist ``pv`` (engine/vocab_prune.py): logits and
+        sampling run over the kept rows and every emitted id is an original token id. JSON-mode
+        requests are refused afterwards (the constraint masks the whole vocabulary)."""
+        from .vocab_prune import apply_vocab_prune
+        apply_vocab_prune(self.model, pv)
+        self._keep = list(pv.keep)
+        self._keep_row = {t: i for i, t in enumerate(self._keep)}
+
     def add_request(self, prompt: List[int], params: Optional[SamplingParams] = None) -> int:
         params = params or SamplingParams()
+        if params.json_mode and getattr(self, "_keep", None) is not None:
+            raise ValueError("JSON mode is not available with a pruned vocabulary")
         if self.prefix_disk is not None and len(prompt) > self._pd_min:
             self._prefix_from_disk(list(map(int, prompt)))
         rid = next(self._ids)
@@ -615,6 +632,13 @@ class Engine:
         # Under tensor parallelism the vocabulary slices are gathered first (every rank, same rows).
         gathered = getattr(m, "gathered_logits", None)
         logits = gathered(max(r for _, r in rows_here) + 1) if gathered is not None else m.logits
+        keep = getattr(self, "_keep", None)
+        if keep is not None:  # pruned head: rows of the logits are kept ids, emitted as original ids
+            return [keep[t] for t in self._sample_rows(rows_here, logits, self._keep_row)]
+        return self._sample_rows(rows_here, logits, None)
+
+    def _sample_rows(self, rows_here, logits, keep_row) -> List[int]:
+        m = self.model
         out = []
         for it, r in rows_here:
             st = self.requests[it.id]
@@ -630,7 +654,10 @@ class Engine:
                 row = logits[r].float().cpu().numpy()
                 s = native().Sampler(p.seed)
                 for t in self.sched.tokens(it.id)[-64:]:
-                    s.record(t)
+                    if keep_row is None:
+                        s.record(t)
+                    elif t in keep_row:
+                        s.record(keep_row[t])
                 sp = native().SamplingParams()
                 sp.temperature, sp.top_k, sp.top_p, sp.repetition_penalty = p.temperature, p.top_k, p.top_p, p.repetition_penalty
                 out.append(int(s.sample(row, sp)))

@@ -289,6 +289,8 @@ class LlamaModel:
         self.status = torch.zeros(1, dtype=torch.int32, device=self.dev)
         self.logit_rows = torch.zeros(R, dtype=torch.int32, device=self.dev)
         self.next_ids = torch.zeros(R, dtype=torch.int32, device=self.dev)
+        # pruned LM head: int32 original token id of every kept head row (None: the full vocabulary)
+        self.vocab_map = None
         self.rope = ops.rope_table(cfg.max_ctx, cfg.rope_dim, cfg.rope_theta, weights.rope_freqs, self.dev)
         self.scale = 1.0 / math.sqrt(hd)
         # sampling inputs (per row)
@@ -349,10 +351,14 @@ class LlamaModel:
         return self.max_rows
 
     def use_tensor_cores(self, rows: int) -> bool:
-        l0 = self.w.layers[0]
-        return rows >= self.tc_min_rows and all(w.fmt == GgmlType.Q4_K for w in l0.wqkv + [l0.wo]) and \
-            l0.moe is None and l0.w_gu is not None and l0.w_gu.fmt == GgmlType.Q4_K and \
-            l0.w_down.fmt == GgmlType.Q4_K
+        if rows < self.tc_min_rows:
+            return False
+        ok = getattr(self, "_tc_layers_ok", None)
+        if ok is None:  # every layer dense Q4_K (a quantisation tier map can mix formats across layers)
+            ok = self._tc_layers_ok = all(
+                all(w.fmt == GgmlType.Q4_K for w in l.wqkv + [l.wo]) and l.moe is None and l.w_gu is not None
+                and l.w_gu.fmt == GgmlType.Q4_K and l.w_down.fmt == GgmlType.Q4_K for l in self.w.layers)
+        return ok
 
     def forward(self, rows: int, sample: str = "greedy", advance: bool = False, n_logits: int = 0):
         """Forward ``rows`` rows from the static inputs; leaves logits and (greedy) next_ids.
@@ -421,7 +427,8 @@ class LlamaModel:
                 ops.advance(inp.ids, self.next_ids, inp.positions, inp.row_ctx, rows)
             return
         # a few sampled rows take the GEMV, unless the tensor-core path was asked for at every size
-        if tc and w.lm_head.fmt == GgmlType.Q4_K and (nl > GEMV_COLS or self.tc_min_rows <= 1):
+        if tc and w.lm_head.fmt == GgmlType.Q4_K and w.lm_head.N % 128 == 0 and \
+                (nl > GEMV_COLS or self.tc_min_rows <= 1):
             ops.rmsnorm(x, w.out_norm, cfg.eps, yb=self.xb[:rows])
             src = self.xb[:rows]
             if n_logits:
@@ -459,6 +466,9 @@ class LlamaModel:
         elif sample == "sample":
             ops.sample(self.logits[:nl], self.temperature[:nl], self.top_k[:nl], self.top_p[:nl],
                        self.rep_penalty[:nl], None, self.uniforms[:nl], self.next_ids[:nl])
+        if self.vocab_map is not None and sample != "none":
+            # pruned head: row index -> original token id, before the id becomes the next input
+            torch.index_select(self.vocab_map, 0, self.next_ids[:nl].long(), out=self.next_ids[:nl])
         if advance:
             ops.advance(inp.ids, self.next_ids, inp.positions, inp.row_ctx, rows)
 

@@ -36,6 +36,12 @@ def main(argv=None):
                     help="speculative decoding: n-gram drafts of up to K tokens when one greedy request decodes")
     ap.add_argument("--prefix-disk", default=None,
                     help="directory of prompt-prefix KV snapshots reused at admission (per rank under TP)")
+    ap.add_argument("--vocab-prune", default=None,
+                    help="JSON whitelist of token ids ({vocab_size_original, keep_token_ids}): the LM head keeps those rows")
+    ap.add_argument("--vocab-first", type=int, default=0,
+                    help="prune the LM head to the first N token ids (plus the end-of-generation ids)")
+    ap.add_argument("--quant-tier-map", default=None,
+                    help="with --gguf: JSON of per-layer FFN formats, re-quantised at load")
     ap.add_argument("--profile", default="default", choices=sorted(RUNTIME_PROFILES),
                     help="runtime profile (lever plan): " + "; ".join(p.contract for p in RUNTIME_PROFILES.values()))
     args = ap.parse_args(argv)
@@ -50,7 +56,7 @@ def main(argv=None):
     device = f"cuda:{int(os.environ.get('LOCAL_RANK', '0'))}" if world > 1 else "cuda"
     if args.gguf:
         eng = Engine.from_gguf(args.gguf, device=device, max_batch=max_batch, max_ctx=args.max_ctx, policy=policy,
-                               tp_rank=rank, tp_world=world, **extra)
+                               tp_rank=rank, tp_world=world, quant_tier_map=args.quant_tier_map, **extra)
         tok = native().Tokenizer.from_gguf(native().GgufFile.open(args.gguf))
         name = args.gguf.rsplit("/", 1)[-1]
     elif args.model:
@@ -64,6 +70,14 @@ def main(argv=None):
                                  device=device, policy=policy, tp_rank=rank, tp_world=world, **extra)
         name = args.preset
     eng.apply_profile(args.profile)
+    if args.vocab_prune or args.vocab_first:
+        if world > 1:
+            ap.error("vocabulary pruning serves on one GPU")
+        from ..engine.vocab_prune import PrunedVocab
+        pv = PrunedVocab.load(args.vocab_prune) if args.vocab_prune else \
+            PrunedVocab.first(args.vocab_first, eng.cfg.vocab, list(tok.eog_ids()))
+        eng.enable_vocab_prune(pv)
+        print(f"LM head pruned to {len(pv)} of {eng.cfg.vocab} tokens", flush=True)
     if args.spec:
         eng.enable_speculative(args.spec)
     if args.prefix_disk:

@@ -90,6 +90,9 @@ class ServeLoop:
                                stop_ids=list(r.stop_ids), json_mode=bool(r.json_mode))
             try:
                 erid = self.engine.add_request(list(r.prompt), p)
+            except ValueError as e:  # a request this engine cannot serve (e.g. JSON mode, pruned vocabulary)
+                self.server.fail(r.id, 400, str(e))
+                continue
             except Exception as e:  # noqa: BLE001
                 self.server.fail(r.id, 500, f"admission failed: {e}")
                 continue
