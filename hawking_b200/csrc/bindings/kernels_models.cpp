@@ -49,10 +49,14 @@ Tensor mixed_descs(const std::vector<Tensor>& codes, const std::vector<Tensor>& 
                                                                                     : (1 << (bits[i] - 1)) - 1)
                                               : 0;
     TORCH_CHECK(kind[i] == hk::MIXED_BINARY ? bits[i] == 1
-                                            : (kind[i] == hk::MIXED_FP8 ? bits[i] == 8
-                                                                        : (bits[i] == 2 || bits[i] == 4 || bits[i] == 8)),
-                "mixed codec: binary (1 bit), uniform 2/4/8 bits or fp8 (8 bits)");
+                                            : (kind[i] == hk::MIXED_FP8 || kind[i] == hk::MIXED_Q4K
+                                                   ? bits[i] == (kind[i] == hk::MIXED_FP8 ? 8 : 4)
+                                                   : (bits[i] == 2 || bits[i] == 4 || bits[i] == 8)),
+                "mixed codec: binary (1 bit), uniform 2/4/8 bits, fp8 (8 bits) or Q4_K (4 bits)");
     TORCH_CHECK(group[i] % 32 == 0, "mixed codec: group must be a multiple of 32");
+    TORCH_CHECK(kind[i] != hk::MIXED_Q4K || (group[i] == 256 && scales[i].stride(0) % 8 == 0 &&
+                                             (reinterpret_cast<uintptr_t>(scales[i].data_ptr()) & 15) == 0),
+                "mixed Q4_K: 256-element super-blocks, 16-byte aligned header rows");
   }
   Tensor out = torch::empty({(int64_t)(n * sizeof(hk::MixedDesc))},
                             torch::TensorOptions().dtype(torch::kUInt8).device(codes.empty() ? torch::kCPU : codes[0].device()));

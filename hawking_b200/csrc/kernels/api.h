@@ -490,7 +490,9 @@ struct MoeGemvArgs {
 void moe_gemv_launch(int fmt, int epi, const MoeGemvArgs& a, cudaStream_t s, bool pdl);
 
 // ---- `.gravity` mixed low-bit codecs (mixed_gemv.cu) ----
-enum MixedKind : int { MIXED_BINARY = 0, MIXED_UNIFORM = 1, MIXED_FP8 = 2 };
+// MIXED_Q4K: a GGUF Q4_K tensor as its two planes (quants [rows, K/2] as codes, the 16-byte
+// super-block headers d | dmin | 12 scale bytes as `scales`, [rows, K/32] halves)
+enum MixedKind : int { MIXED_BINARY = 0, MIXED_UNIFORM = 1, MIXED_FP8 = 2, MIXED_Q4K = 3 };
 struct MixedDesc {            // one weight tensor [rows, K] in device memory
   const uint8_t* codes;       // LSB-first code stream per row
   const __half* scales;       // fp16 group scales per row (binary / uniform)

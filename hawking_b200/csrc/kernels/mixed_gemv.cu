@@ -42,7 +42,6 @@ __device__ __forceinline__ uint32_t spread2(uint32_t byte) {
 __device__ __forceinline__ float mixed_block_dot(const MixedDesc& t, int64_t row, int blk, const int8_t* xq,
                                                   float dx, float sx) {
   const uint8_t* codes = t.codes + row * t.code_row_bytes;
-  const float sg = t.kind == MIXED_FP8 ? 0.f : __half2float(t.scales[row * t.scale_row_elems + (blk * 32) / t.group]);
   const int4 qa = *reinterpret_cast<const int4*>(xq + blk * 32);
   const int4 qb = *reinterpret_cast<const int4*>(xq + blk * 32 + 16);
   const int q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
@@ -66,6 +65,24 @@ __device__ __forceinline__ float mixed_block_dot(const MixedDesc& t, int64_t row
     (void)sx;
     return sw * dx * acc;
   }
+  if (t.kind == MIXED_Q4K) {
+    // GGUF Q4_K sub-block j of super-block sb: w = d * sc_j * q - dmin * m_j, q the low (even j) or
+    // high (odd j) nibbles of the 32 quant bytes the sub-block pair shares
+    const int sb = blk >> 3, j = blk & 7;
+    const uint4 h = __ldg(reinterpret_cast<const uint4*>(t.scales + row * t.scale_row_elems) + sb);
+    int sc, mn;
+    q4k_scale_min(j, h.y, h.z, h.w, sc, mn);
+    const float d = __half2float(__ushort_as_half((unsigned short)(h.x & 0xFFFFu)));
+    const float dmin = __half2float(__ushort_as_half((unsigned short)(h.x >> 16)));
+    const uint4* qp = reinterpret_cast<const uint4*>(codes + sb * 128 + (j >> 1) * 32);
+    const uint4 w0 = __ldg(qp), w1 = __ldg(qp + 1);
+    const uint32_t ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    const int sh = (j & 1) * 4;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) dot = dp4a((int)((ws[k] >> sh) & 0x0F0F0F0Fu), q[k], dot);
+    return d * (float)sc * dx * (float)dot - dmin * (float)mn * sx;
+  }
+  const float sg = __half2float(t.scales[row * t.scale_row_elems + (blk * 32) / t.group]);
   if (t.kind == MIXED_BINARY) {
     const uint32_t b = __ldg(reinterpret_cast<const uint32_t*>(codes) + blk);
 #pragma unroll

@@ -212,6 +212,10 @@ class Engine:
         ph["config"] = (time.perf_counter() - t) * 1e3
         free, _ = torch.cuda.mem_get_info(device)
         check_memory_budget(sum(ti.nbytes for ti in m.tensors.values()), free, f"weights of {path}")
+        if cfg.arch == "deepseek2":
+            return Engine._deepseek_from_gguf(m, cfg, path, device, max_batch, tp_rank, tp_world, ph, timing,
+                                              **{k: v for k, v in kw.items()
+                                                 if k in ("block_size", "num_blocks", "kv_fraction", "policy")})
         t = time.perf_counter()
         w = load_llama_weights(m, cfg, device)
         if quant_tier_map:
@@ -228,6 +232,30 @@ class Engine:
                                tp=tp, **kw)
         else:
             eng = Engine.build(cfg, w, device=device, max_batch=max_batch, max_ctx=max_ctx, **kw)
+        ph["engine"] = (time.perf_counter() - t) * 1e3
+        eng.startup = {k: round(v, 2) for k, v in ph.items()}
+        if timing:
+            print(json.dumps({"startup_ms": eng.startup, "path": path}), file=sys.stderr, flush=True)
+        return eng
+
+    @staticmethod
+    def _deepseek_from_gguf(m, cfg, path, device, max_batch, tp_rank, tp_world, ph, timing, **kw):
+        """The MLA + MoE engine over a ``deepseek2`` GGUF (models/deepseek_gguf.py); under
+        ``tp_world > 1`` this rank's head / expert shard."""
+        from ..models.deepseek_gguf import load_deepseek_weights
+        t = time.perf_counter()
+        w = load_deepseek_weights(m, cfg, device)
+        ph["weights"] = (time.perf_counter() - t) * 1e3
+        t = time.perf_counter()
+        if tp_world > 1:
+            from ..parallel.ep import local_deepseek_config, shard_deepseek_weights
+            from ..parallel.tp import TPComm
+            w = shard_deepseek_weights(w, cfg, tp_rank, tp_world)
+            tp = TPComm(tp_rank, tp_world, 2 * cfg.layers, 8, cfg.hidden, torch.device(device))
+            eng = Engine.build_deepseek(local_deepseek_config(cfg, tp_world), w, device=device, max_batch=max_batch,
+                                        tp=tp, **kw)
+        else:
+            eng = Engine.build_deepseek(cfg, w, device=device, max_batch=max_batch, **kw)
         ph["engine"] = (time.perf_counter() - t) * 1e3
         eng.startup = {k: round(v, 2) for k, v in ph.items()}
         if timing:

@@ -155,6 +155,92 @@ def write_llama_family_gguf(path: str, cfg: ModelConfig, seed: int = 0, std: flo
     return b.write(path)
 
 
+def write_deepseek2_gguf(path: str, cfg: ModelConfig, seed: int = 0, std: float = 0.02, mix: bool = True,
+                         yarn: float = 0.0, threads: int = 8) -> str:
+    """A ``deepseek2`` GGUF (MLA + MoE, llama.cpp tensor names) of random N(0, std) weights. The
+    projections take ``cfg.weight_type``; with ``mix`` the routed experts' down projections and
+    the LM head are Q6_K, the shared experts Q8_0 and the dense FFN Q4_0 (every loader mapping is
+    exercised). ``yarn`` > 1 writes YaRN rope-scaling keys with that factor."""
+    rng = np.random.default_rng(seed)
+    wt = type_id(cfg.weight_type)
+    b = GgufBuilder("deepseek2")
+    b.set("general.name", "synthetic-deepseek2")
+    toks, merges, bos, eos = synthetic_bpe_vocab(cfg.vocab)
+    b.set("tokenizer.ggml.model", "gpt2")
+    b.set("tokenizer.ggml.pre", "llama-bpe")
+    b.set("tokenizer.ggml.tokens", toks)
+    b.set("tokenizer.ggml.merges", merges)
+    b.set("tokenizer.ggml.bos_token_id", bos, 4)
+    b.set("tokenizer.ggml.eos_token_id", eos, 4)
+    H, nh, nope, rd, vd = cfg.hidden, cfg.n_heads, cfg.qk_nope_dim, cfg.qk_rope_dim, cfg.v_head_dim
+    E, Fe, ns = cfg.n_experts, cfg.expert_ffn, cfg.n_shared_experts
+    for k, v in (("vocab_size", cfg.vocab), ("context_length", cfg.max_ctx), ("embedding_length", H),
+                 ("block_count", cfg.layers), ("feed_forward_length", cfg.ffn), ("attention.head_count", nh),
+                 ("attention.head_count_kv", nh), ("attention.key_length", nope + rd),
+                 ("attention.value_length", vd), ("rope.dimension_count", rd),
+                 ("attention.kv_lora_rank", cfg.kv_lora_rank), ("leading_dense_block_count", cfg.first_dense_layers),
+                 ("expert_count", E), ("expert_used_count", cfg.top_k), ("expert_shared_count", ns),
+                 ("expert_feed_forward_length", Fe), ("expert_group_count", cfg.n_groups),
+                 ("expert_group_used_count", cfg.topk_groups),
+                 ("expert_gating_func", 2 if cfg.router == "sigmoid_bias" else 1)):
+        b.arch_set(k, v)
+    if cfg.q_lora_rank:
+        b.arch_set("attention.q_lora_rank", cfg.q_lora_rank)
+    b.arch_set("expert_weights_norm", bool(cfg.norm_topk))
+    b.set_f32("deepseek2.expert_weights_scale", cfg.routed_scale)
+    b.set_f32("deepseek2.rope.freq_base", cfg.rope_theta)
+    b.set_f32("deepseek2.attention.layer_norm_rms_epsilon", cfg.eps)
+    if yarn > 1.0:
+        b.set("deepseek2.rope.scaling.type", "yarn")
+        b.set_f32("deepseek2.rope.scaling.factor", yarn)
+        b.arch_set("rope.scaling.original_context_length", max(cfg.max_ctx // 4, 64))
+        b.set_f32("deepseek2.rope.scaling.yarn_log_multiplier", 0.1)
+
+    def w(*shape):
+        return (rng.standard_normal(shape, dtype=np.float32) * std).astype(np.float32)
+
+    def norm(n):
+        return (1.0 + 0.1 * rng.standard_normal(n)).astype(np.float32)
+
+    t6 = GgmlType.Q6_K if mix else wt
+    t8 = GgmlType.Q8_0 if mix else wt
+    t40 = GgmlType.Q4_0 if mix else wt
+    b.add("token_embd.weight", w(cfg.vocab, H), GgmlType.F16)
+    for l in range(cfg.layers):
+        p = f"blk.{l}."
+        b.add(p + "attn_norm.weight", norm(H), GgmlType.F32)
+        if cfg.q_lora_rank:
+            b.add(p + "attn_q_a.weight", w(cfg.q_lora_rank, H), wt, threads)
+            b.add(p + "attn_q_a_norm.weight", norm(cfg.q_lora_rank), GgmlType.F32)
+            b.add(p + "attn_q_b.weight", w(nh * (nope + rd), cfg.q_lora_rank), wt, threads)
+        else:
+            b.add(p + "attn_q.weight", w(nh * (nope + rd), H), wt, threads)
+        b.add(p + "attn_kv_a_mqa.weight", w(cfg.kv_lora_rank + rd, H), wt, threads)
+        b.add(p + "attn_kv_a_norm.weight", norm(cfg.kv_lora_rank), GgmlType.F32)
+        b.add(p + "attn_kv_b.weight", w(nh * (nope + vd), cfg.kv_lora_rank), wt, threads)
+        b.add(p + "attn_output.weight", w(H, nh * vd), wt, threads)
+        b.add(p + "ffn_norm.weight", norm(H), GgmlType.F32)
+        if l < cfg.first_dense_layers:
+            b.add(p + "ffn_gate.weight", w(cfg.ffn, H), t40, threads)
+            b.add(p + "ffn_up.weight", w(cfg.ffn, H), t40, threads)
+            b.add(p + "ffn_down.weight", w(H, cfg.ffn), t40, threads)
+            continue
+        # softmax routers get a wide logit spread (decisive top-k); sigmoid scores would saturate
+        b.add(p + "ffn_gate_inp.weight", w(E, H) * (1 if cfg.router == "sigmoid_bias" else 5), GgmlType.F32)
+        if cfg.router == "sigmoid_bias":
+            b.add(p + "exp_probs_b.bias", (0.01 * rng.standard_normal(E)).astype(np.float32), GgmlType.F32)
+        b.add(p + "ffn_gate_exps.weight", w(E, Fe, H), wt, threads)
+        b.add(p + "ffn_up_exps.weight", w(E, Fe, H), wt, threads)
+        b.add(p + "ffn_down_exps.weight", w(E, H, Fe), t6, threads)
+        if ns:
+            b.add(p + "ffn_gate_shexp.weight", w(ns * Fe, H), t8, threads)
+            b.add(p + "ffn_up_shexp.weight", w(ns * Fe, H), t8, threads)
+            b.add(p + "ffn_down_shexp.weight", w(H, ns * Fe), t8, threads)
+    b.add("output_norm.weight", norm(H), GgmlType.F32)
+    b.add("output.weight", w(cfg.vocab, H), t6, threads)
+    return b.write(path)
+
+
 def write_tokenizer_gguf(path: str, vocab: int, arch: str = "llama") -> str:
     """A GGUF file holding only the synthetic byte-level BPE tokenizer of ``vocab`` tokens (no
     tensors): the tokenizer for models built from random weights without a GGUF of their own."""

@@ -55,6 +55,10 @@ class ModelConfig:
     qk_nope_dim: int = 0
     qk_rope_dim: int = 0
     v_head_dim: int = 0
+    # YaRN rope scaling (0: none): scale factor, original context, attention-scale log multiplier
+    rope_yarn_factor: float = 0.0
+    rope_yarn_orig_ctx: int = 0
+    rope_yarn_log_mul: float = 0.0
     # storage
     weight_type: str = "Q4_K"
     embed_type: str = ""             # "" = same as weight_type

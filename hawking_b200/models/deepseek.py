@@ -158,7 +158,7 @@ class DeepSeekModel:
         self.xa = Q8Act(R, H, dev)
         self.qakva = torch.zeros(R, cfg.q_lora_rank + LAT + ROPE, device=dev)
         self.qa = self.qakva[:, :cfg.q_lora_rank]
-        self.qaq = Q8Act(R, cfg.q_lora_rank, dev)
+        self.qaq = Q8Act(R, cfg.q_lora_rank, dev) if cfg.q_lora_rank else None
         self.q = torch.zeros(R, nh * (nope + rd), device=dev)
         self.kva = self.qakva[:, cfg.q_lora_rank:]
         self.q_lat = torch.zeros(R, nh, LAT, device=dev)
@@ -183,8 +183,10 @@ class DeepSeekModel:
         self.hs = Q8Act(R, Fs, dev)
         self.logits = torch.zeros(R, cfg.vocab, device=dev)
         self.next_ids = torch.zeros(R, dtype=torch.int32, device=dev)
-        self.rope = ops.rope_table(cfg.max_ctx, ROPE, cfg.rope_theta, None, dev)
-        self.scale = 1.0 / math.sqrt(nope + rd)
+        from .deepseek_gguf import yarn_attention_scale, yarn_freq_factors
+        self.rope = ops.rope_table(cfg.max_ctx, ROPE, cfg.rope_theta, yarn_freq_factors(cfg), dev)
+        self.scale = yarn_attention_scale(cfg)
+        self.scoring = 1 if cfg.router == "sigmoid_bias" else 0  # router: sigmoid + bias, or softmax
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
         if tp is not None:
             self.x2 = torch.zeros(R, H, device=dev)  # second residual buffer of the push all-reduce
@@ -208,9 +210,17 @@ class DeepSeekModel:
         cfg, t, kv, inp = self.cfg, self.w.table, self.kv, self.inp
         K = kernels()
         xa = self.xa.view(rows)
-        mixed_gemv(t, L.idx["qakva"], xa, self.qakva[:rows])
-        ops.rmsnorm_q8(self.qa[:rows], L.q_a_norm, cfg.eps, self.qaq.view(rows))
-        mixed_gemv(t, L.idx["qb"], self.qaq.view(rows), self.q[:rows])
+        if "q" in L.idx:  # no query low-rank: q and kv_a straight from the normed hidden
+            mixed_gemv(t, L.idx["q"], xa, self.q[:rows])
+            mixed_gemv(t, L.idx["kva"], xa, self.kva[:rows])
+        else:
+            if "qakva" in L.idx:
+                mixed_gemv(t, L.idx["qakva"], xa, self.qakva[:rows])
+            else:
+                mixed_gemv(t, L.idx["qa"], xa, self.qa[:rows])
+                mixed_gemv(t, L.idx["kva"], xa, self.kva[:rows])
+            ops.rmsnorm_q8(self.qa[:rows], L.q_a_norm, cfg.eps, self.qaq.view(rows))
+            mixed_gemv(t, L.idx["qb"], self.qaq.view(rows), self.q[:rows])
         ops.launches.add(4)
         K.mla_kv_append(self.kva[:rows], L.kv_a_norm, cfg.eps, inp.positions[:rows], kv.block_tables,
                         inp.row_seq[:rows], self.rope, kv.latent[l], ops.PDL)
@@ -253,7 +263,7 @@ class DeepSeekModel:
         if self.fused_route:
             # one launch: router GEMV, top-k, sort by expert, active list (this rank's experts only
             # under expert parallelism); experts read token rows
-            ops.moe_route(L.router, xa, k, 1, L.router_bias, cfg.n_groups, cfg.topk_groups, cfg.norm_topk,
+            ops.moe_route(L.router, xa, k, self.scoring, L.router_bias, cfg.n_groups, cfg.topk_groups, cfg.norm_topk,
                           cfg.routed_scale, self.rlog[:rows], self.ids[:rows], self.rw[:rows], self.counts,
                           self.offsets, self.sorted, self.active, self.n_active, fold, self.route_counter,
                           e_lo=e_lo, e_hi=e_lo + ne if self.w.e_count else 0)
@@ -262,7 +272,7 @@ class DeepSeekModel:
             if self.w.e_count:
                 raise NotImplementedError("expert parallel needs the fused routing kernel")
             ops.router_logits(L.router, xa, self.rlog[:rows])
-            ops.moe_topk(self.rlog[:rows], L.router_bias, k, 1, cfg.n_groups, cfg.topk_groups, cfg.norm_topk,
+            ops.moe_topk(self.rlog[:rows], L.router_bias, k, self.scoring, cfg.n_groups, cfg.topk_groups, cfg.norm_topk,
                          cfg.routed_scale, self.ids[:rows], self.rw[:rows])
             ops.moe_align(self.ids[:rows], E, xa, self.counts, self.offsets, self.sorted, self.gx, shared=fold)
             ops.launches.add()
@@ -284,7 +294,7 @@ class DeepSeekModel:
         K.moe_mixed_gemv(1, t.descs, L.idx["ed"], L.idx["ed"], H, F, k, self.counts, self.offsets, self.sorted,
                          self.active, self.n_active, na, self.hx.q, self.hx.d, self.hx.s, None, None, None,
                          self.x[:rows], self.rw[:rows].reshape(-1), ops.PDL, rows * k, **ep)
-        if not fold:
+        if not fold and "sg" in L.idx:
             hs = self.hs.view(rows)
             mixed_gemv_swiglu(t, L.idx["sg"], L.idx["su"], xa, hs)
             mixed_gemv(t, L.idx["sd"], hs, self.x[:rows], residual=True)
@@ -437,7 +447,9 @@ class TorchRefDeepSeek:
     the latent per head, as in the reference CPU oracle) and the device's activation rounding."""
 
     def __init__(self, cfg: ModelConfig, w: DSWeights, act_q8: bool = True):
+        from .deepseek_gguf import yarn_attention_scale
         self.cfg, self.w, self.act_q8 = cfg, w, act_q8
+        self.scale = yarn_attention_scale(cfg)
         self.W = [mw.dequantize() for mw in w.table.weights]
         self.E = w.embed.dequantize()
         self.cache = {l: [] for l in range(cfg.layers)}
@@ -455,7 +467,11 @@ class TorchRefDeepSeek:
         return x * torch.rsqrt((x * x).mean() + eps) * w
 
     def _rope(self, x, pos):
+        from .deepseek_gguf import yarn_freq_factors
         inv = 1.0 / (self.cfg.rope_theta ** (torch.arange(0, ROPE, 2, device=x.device, dtype=torch.float64) / ROPE))
+        ff = yarn_freq_factors(self.cfg)
+        if ff is not None:
+            inv = inv / ff.to(inv.device)
         ang = (pos * inv).float()
         c, s = torch.cos(ang), torch.sin(ang)
         a, b = x[..., :ROPE // 2], x[..., ROPE // 2:]
@@ -464,8 +480,12 @@ class TorchRefDeepSeek:
     def _route(self, L, h):
         cfg = self.cfg
         logits = L.router @ h
-        s = torch.sigmoid(logits)
-        choice = s + L.router_bias
+        if cfg.router == "sigmoid_bias":
+            s = torch.sigmoid(logits)
+            choice = s + L.router_bias if L.router_bias is not None else s
+        else:
+            s = torch.softmax(logits.double(), 0).float()
+            choice = s
         E, ng = cfg.n_experts, cfg.n_groups
         gs = choice.view(ng, E // ng).topk(2, dim=1).values.sum(1)
         keep = torch.zeros(ng, dtype=torch.bool, device=h.device)
@@ -483,8 +503,11 @@ class TorchRefDeepSeek:
         x = self.E[token].clone()
         for l, L in enumerate(w.layers):
             h = self._q(self._rms(x, L.attn_norm, cfg.eps))
-            qa = W[L.idx["qa"]] @ h
-            q = (W[L.idx["qb"]] @ self._q(self._rms(qa, L.q_a_norm, cfg.eps))).view(nh, nope + rd)
+            if "q" in L.idx:
+                q = (W[L.idx["q"]] @ h).view(nh, nope + rd)
+            else:
+                qa = W[L.idx["qa"]] @ h
+                q = (W[L.idx["qb"]] @ self._q(self._rms(qa, L.q_a_norm, cfg.eps))).view(nh, nope + rd)
             kva = W[L.idx["kva"]] @ h
             c = self._rms(kva[:LAT], L.kv_a_norm, cfg.eps).bfloat16().float()
             kpe = self._rope(kva[LAT:], pos).bfloat16().float()
@@ -497,7 +520,7 @@ class TorchRefDeepSeek:
                 k_nope = C @ uk[i].t()                          # [T, nope]
                 v = C @ uv[i].t()                               # [T, vd]
                 qpe = self._rope(q[i, nope:], pos)
-                sc = (k_nope @ q[i, :nope] + KP @ qpe) / math.sqrt(nope + rd)
+                sc = (k_nope @ q[i, :nope] + KP @ qpe) * self.scale
                 o[i] = torch.softmax(sc, 0) @ v
             x = x + W[L.idx["o"]] @ self._q(o.reshape(-1))
             h = self._q(self._rms(x, L.ffn_norm, cfg.eps))
@@ -509,7 +532,8 @@ class TorchRefDeepSeek:
                 for e, wt in zip(idx, wts):
                     gt, up = W[L.idx["eg"] + e] @ h, W[L.idx["eu"] + e] @ h
                     x = x + wt * (W[L.idx["ed"] + e] @ self._q(gt / (1 + torch.exp(-gt)) * up))
-                gt, up = W[L.idx["sg"]] @ h, W[L.idx["su"]] @ h
-                x = x + W[L.idx["sd"]] @ self._q(gt / (1 + torch.exp(-gt)) * up)
+                if "sg" in L.idx:
+                    gt, up = W[L.idx["sg"]] @ h, W[L.idx["su"]] @ h
+                    x = x + W[L.idx["sd"]] @ self._q(gt / (1 + torch.exp(-gt)) * up)
         h = self._q(self._rms(x, w.out_norm, cfg.eps))
         return W[w.lm_head] @ h

@@ -47,6 +47,9 @@ def rmsnorm_ref(x: torch.Tensor, w: Optional[torch.Tensor], eps: float) -> torch
 
 def config_from_gguf(m: GgufModel) -> ModelConfig:
     a = m.architecture
+    if a == "deepseek2":
+        from .deepseek_gguf import deepseek_config_from_gguf
+        return deepseek_config_from_gguf(m)
     g = lambda k, d=None: m.get(f"{a}.{k}", d)  # noqa: E731
     hidden = int(g("embedding_length"))
     nh = int(g("attention.head_count"))

@@ -19,7 +19,7 @@ import torch
 
 from .._ext import kernels
 
-BINARY, UNIFORM, FP8 = 0, 1, 2
+BINARY, UNIFORM, FP8, Q4K = 0, 1, 2, 3  # Q4K: a GGUF Q4_K tensor's quant + header planes
 
 
 def _pack_lsb(codes: torch.Tensor, bits: int) -> torch.Tensor:
@@ -148,7 +148,44 @@ class MixedWeight:
         codes = torch.from_numpy(body[groups * 2:].copy().reshape(rows, cols * bits // 8))
         return MixedWeight(kind, bits, gs, rows, cols, codes.to(device).contiguous(), scales.to(device).contiguous())
 
+    @staticmethod
+    def from_gguf(raw: torch.Tensor, fmt: int, N: int, K: int, device) -> "MixedWeight":
+        """A GGUF tensor's bytes ([N, row_bytes] uint8, any device) as a table weight. Q4_K keeps
+        its own planes (kind Q4K), Q8_0 becomes 8-bit codes q + 128 with its fp16 block scales and
+        Q4_0 4-bit codes (zero point 8) with its nibbles re-ordered LSB-first: all three are the
+        file's values bit for bit. Other formats are decoded and re-encoded as 8-bit codes with
+        one fp16 scale per 32 elements (absmax / 127; error at most half a code step)."""
+        from ..formats.ggml import GgmlType
+        from .qweight import QWeight
+        fmt = int(fmt)
+        raw = raw.to(device)
+        if fmt == GgmlType.Q4_K:
+            q = QWeight.from_raw(raw, fmt, N, K)
+            return MixedWeight(Q4K, 4, 256, N, K, q.planes[0].contiguous(),
+                               q.planes[1].contiguous().view(torch.float16))
+        if fmt == GgmlType.Q8_0:
+            b = raw.reshape(N, K // 32, 34)
+            scales = b[:, :, :2].contiguous().view(torch.float16).reshape(N, K // 32)
+            codes = (b[:, :, 2:] ^ 0x80).reshape(N, K)
+            return MixedWeight(UNIFORM, 8, 32, N, K, codes.contiguous(), scales.contiguous(), zero=128)
+        if fmt == GgmlType.Q4_0:
+            b = raw.reshape(N, K // 32, 18)
+            scales = b[:, :, :2].contiguous().view(torch.float16).reshape(N, K // 32)
+            qs = b[:, :, 2:].to(torch.int32)
+            nib = torch.cat([qs & 0xF, qs >> 4], -1).reshape(N, K)  # element i: low nibble i, i + 16: high
+            return MixedWeight(UNIFORM, 4, 32, N, K, _pack_lsb(nib, 4).contiguous(), scales.contiguous(), zero=8)
+        from ..formats import quant_torch
+        w = quant_torch.dequantize(raw, fmt, (N, K)).float()
+        return MixedWeight.quantize(w, UNIFORM, bits=8, group=32)
+
     def dequantize(self) -> torch.Tensor:
+        if self.kind == Q4K:
+            from ..formats import quant_torch
+            from ..formats.ggml import GgmlType
+            nb = self.K // 256
+            raw = torch.cat([self.scales.view(torch.uint8).reshape(self.N, nb, 16),
+                             self.codes.reshape(self.N, nb, 128)], -1).reshape(self.N, nb * 144)
+            return quant_torch.dequantize(raw, GgmlType.Q4_K, (self.N, self.K)).float()
         if self.kind == FP8:
             return self.codes.view(torch.float8_e4m3fn).float() * self.scales.repeat_interleave(self.group, 1)
         c = _unpack_lsb(self.codes, self.bits, self.K).float()
@@ -167,8 +204,9 @@ class MixedWeight:
         if k0 % self.group or k1 % self.group or k0 % 32 or k1 % 32:
             raise ValueError("column slice must align to the scale groups and 32-element blocks")
         b0, b1 = k0 * self.bits // 8, k1 * self.bits // 8
+        s0, s1 = (k0 // 32, k1 // 32) if self.kind == Q4K else (k0 // self.group, k1 // self.group)
         return MixedWeight(self.kind, self.bits, self.group, self.N, k1 - k0, self.codes[:, b0:b1].contiguous(),
-                           self.scales[:, k0 // self.group:k1 // self.group].contiguous(), self.zero)
+                           self.scales[:, s0:s1].contiguous(), self.zero)
 
     def contiguous(self) -> "MixedWeight":
         return MixedWeight(self.kind, self.bits, self.group, self.N, self.K, self.codes.contiguous(),

@@ -67,10 +67,12 @@ def shard_deepseek_weights(w: DSWeights, cfg: ModelConfig, rank: int, world: int
         nl = DSLayer(L.dense, L.attn_norm, L.q_a_norm, L.kv_a_norm, L.ffn_norm,
                      w_uk=L.w_uk[h0:h1].contiguous(), w_uv=L.w_uv[h0:h1].contiguous(),
                      router=L.router, router_bias=L.router_bias)
-        nl.idx["qakva"] = put(W[L.idx["qakva"]])
-        nl.idx["qa"] = put(W[L.idx["qa"]])
-        nl.idx["kva"] = put(W[L.idx["kva"]])
-        nl.idx["qb"] = put(W[L.idx["qb"]].rows(h0 * qk, lnh * qk).contiguous())
+        for key in ("qakva", "qa", "kva"):  # replicated (q_a / kv_a, or kv_a alone without q low-rank)
+            if key in L.idx:
+                nl.idx[key] = put(W[L.idx[key]])
+        for key in ("qb", "q"):  # query heads split
+            if key in L.idx:
+                nl.idx[key] = put(W[L.idx[key]].rows(h0 * qk, lnh * qk).contiguous())
         nl.idx["o"] = put(W[L.idx["o"]].cols(h0 * vd, h1 * vd))
         if L.dense:
             nl.idx["g"] = put(W[L.idx["g"]].rows(rank * lF, lF).contiguous())
@@ -82,7 +84,7 @@ def shard_deepseek_weights(w: DSWeights, cfg: ModelConfig, rank: int, world: int
                 nl.idx[m] = len(ws)
                 for e in range(e_lo, e_lo + ne):
                     put(W[L.idx[m] + e])
-                if nl.shared_here:  # the shared expert follows this rank's routed experts
+                if nl.shared_here and sm in L.idx:  # the shared expert follows this rank's routed experts
                     nl.idx[sm] = put(W[L.idx[sm]])
         layers.append(nl)
     V = cfg.vocab // world

@@ -1,0 +1,152 @@
+"""A ``deepseek2`` GGUF through the engine: the MLA + MoE decode forward over the file's weights
+agrees with (a) the engine's own fp32 restatement on the loaded tables (tight, same activation
+rounding) and (b) an independent fp32 forward written from the GGUF's dequantised tensors with the
+file's adjacent-pair RoPE and un-absorbed MLA (loose: no activation rounding). Two variants: a
+V3-style file (query low-rank, sigmoid + bias group routing, YaRN, mixed Q4_K / Q6_K / Q8_0 /
+Q4_0 tensors) and a V2-Lite-style file (plain query projection, softmax routing, two shared
+experts)."""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+from hawking_b200.engine.engine import Engine  # noqa: E402
+from hawking_b200.engine.sampling import SamplingParams  # noqa: E402
+from hawking_b200.formats.gguf import GgufModel  # noqa: E402
+from hawking_b200.formats.synth import random_prompt, write_deepseek2_gguf  # noqa: E402
+from hawking_b200.models.config import preset  # noqa: E402
+from hawking_b200.models.deepseek import TorchRefDeepSeek  # noqa: E402
+from hawking_b200.models.deepseek_gguf import yarn_attention_scale, yarn_freq_factors  # noqa: E402
+
+DEV = "cuda"
+
+
+def _cfg(**kw):
+    base = dict(vocab=2048, hidden=512, layers=3, n_heads=4, n_kv_heads=4, ffn=512, n_experts=8, top_k=2,
+                expert_ffn=256, shared_ffn=256, n_groups=4, topk_groups=2, first_dense_layers=1, q_lora_rank=256,
+                max_ctx=512, weight_type="Q4_K")
+    base.update(kw)
+    return preset("deepseek-v3").with_(**base)
+
+
+VARIANTS = {
+    "v3": (_cfg(), 4.0),
+    "v2lite": (_cfg(q_lora_rank=0, router="softmax", n_groups=1, topk_groups=1, norm_topk=False, routed_scale=1.0,
+                    n_shared_experts=2, shared_ffn=512), 0.0),
+}
+
+
+class FileOracle:
+    """fp32 token-serial forward from the GGUF's dequantised tensors (file conventions)."""
+
+    def __init__(self, path, cfg):
+        self.m, self.cfg = GgufModel(path), cfg
+        self.W = {n: torch.from_numpy(self.m.dequantize(n).copy()).float().to(DEV) for n in self.m.tensors}
+        c = cfg
+        inv = 1.0 / (c.rope_theta ** (torch.arange(0, c.qk_rope_dim, 2, dtype=torch.float64) / c.qk_rope_dim))
+        ff = yarn_freq_factors(c)
+        self.inv = (inv / ff if ff is not None else inv).to(DEV)
+        self.scale = yarn_attention_scale(c)
+        self.cache = {l: [] for l in range(c.layers)}
+
+    def rope(self, x, pos):  # adjacent pairs
+        ang = (pos * self.inv).float()
+        a, b = x[..., 0::2], x[..., 1::2]
+        out = torch.empty_like(x)
+        out[..., 0::2] = a * torch.cos(ang) - b * torch.sin(ang)
+        out[..., 1::2] = b * torch.cos(ang) + a * torch.sin(ang)
+        return out
+
+    @staticmethod
+    def rms(x, w, eps):
+        return x * torch.rsqrt((x * x).mean() + eps) * w
+
+    def ffn(self, p, h):
+        W, c = self.W, self.cfg
+        silu = torch.nn.functional.silu
+        if p + "ffn_gate.weight" in W:
+            return W[p + "ffn_down.weight"] @ (silu(W[p + "ffn_gate.weight"] @ h) * (W[p + "ffn_up.weight"] @ h))
+        logits = W[p + "ffn_gate_inp.weight"] @ h
+        E = c.n_experts
+        if c.router == "sigmoid_bias":
+            s = torch.sigmoid(logits)
+            sel = s + W[p + "exp_probs_b.bias"]
+        else:
+            s = torch.softmax(logits.double(), 0).float()
+            sel = s.clone()
+        if c.n_groups > 1:
+            gs = sel.view(c.n_groups, E // c.n_groups).topk(2, dim=1).values.sum(1)
+            keep = torch.zeros(c.n_groups, dtype=torch.bool, device=DEV)
+            keep[gs.topk(c.topk_groups).indices] = True
+            sel = torch.where(keep.repeat_interleave(E // c.n_groups), sel, torch.full_like(sel, -float("inf")))
+        idx = sel.topk(c.top_k).indices
+        wts = s[idx]
+        if c.norm_topk:
+            wts = wts / wts.sum()
+        wts = wts * c.routed_scale
+        out = torch.zeros_like(h)
+        for e, wt in zip(idx.tolist(), wts):
+            g = W[p + "ffn_gate_exps.weight"][e] @ h
+            u = W[p + "ffn_up_exps.weight"][e] @ h
+            out = out + wt * (W[p + "ffn_down_exps.weight"][e] @ (silu(g) * u))
+        if p + "ffn_gate_shexp.weight" in W:
+            out = out + W[p + "ffn_down_shexp.weight"] @ (silu(W[p + "ffn_gate_shexp.weight"] @ h) *
+                                                          (W[p + "ffn_up_shexp.weight"] @ h))
+        return out
+
+    def step(self, tok, pos):
+        W, c = self.W, self.cfg
+        nh, nope, rd, vd = c.n_heads, c.qk_nope_dim, c.qk_rope_dim, c.v_head_dim
+        x = W["token_embd.weight"][tok].clone()
+        for l in range(c.layers):
+            p = f"blk.{l}."
+            h = self.rms(x, W[p + "attn_norm.weight"], c.eps)
+            if c.q_lora_rank:
+                qa = self.rms(W[p + "attn_q_a.weight"] @ h, W[p + "attn_q_a_norm.weight"], c.eps)
+                q = (W[p + "attn_q_b.weight"] @ qa).view(nh, nope + rd)
+            else:
+                q = (W[p + "attn_q.weight"] @ h).view(nh, nope + rd)
+            kva = W[p + "attn_kv_a_mqa.weight"] @ h
+            cl = self.rms(kva[:512], W[p + "attn_kv_a_norm.weight"], c.eps)
+            self.cache[l].append((cl, self.rope(kva[512:], pos)))
+            C = torch.stack([a for a, _ in self.cache[l]])
+            KP = torch.stack([b for _, b in self.cache[l]])
+            kvb = W[p + "attn_kv_b.weight"].view(nh, nope + vd, 512)
+            o = torch.empty(nh, vd, device=DEV)
+            for i in range(nh):
+                sc = (C @ kvb[i, :nope].t() @ q[i, :nope] + KP @ self.rope(q[i, nope:], pos)) * self.scale
+                o[i] = torch.softmax(sc, 0) @ (C @ kvb[i, nope:].t())
+            x = x + W[p + "attn_output.weight"] @ o.reshape(-1)
+            x = x + self.ffn(p, self.rms(x, W[p + "ffn_norm.weight"], c.eps))
+        return W["output.weight"] @ self.rms(x, W["output_norm.weight"], c.eps)
+
+
+@pytest.mark.parametrize("variant", sorted(VARIANTS))
+def test_deepseek2_gguf_decode_matches_oracles(tmp_path, variant):
+    cfg, yarn = VARIANTS[variant]
+    path = write_deepseek2_gguf(str(tmp_path / "ds.gguf"), cfg, seed=11, std=0.05, yarn=yarn)
+    eng = Engine.from_gguf(path, device=DEV, max_batch=2, max_ctx=256, block_size=64, num_blocks=16)
+    model = eng.model
+    assert model.cfg.arch == "deepseek2" and model.cfg.q_lora_rank == cfg.q_lora_rank
+    prompt = random_prompt(20, cfg.vocab, seed=12)
+    got = model.forward_tokens(prompt, seq_id=1)
+    torch.cuda.synchronize()
+    with torch.no_grad():
+        ref_tab = TorchRefDeepSeek(model.cfg, model.w, act_q8=True)
+        tab = torch.stack([ref_tab.step(t, i) for i, t in enumerate(prompt)])
+        ora = FileOracle(path, model.cfg)
+        fil = torch.stack([ora.step(t, i) for i, t in enumerate(prompt)])
+    scale = fil.abs().max().item()
+    # per position: a near-tie in a top-k expert choice can flip between two correct forwards (the
+    # router sees activations that differ by rounding) and moves that position's logits a lot, so
+    # at least 3/4 of the positions must match closely rather than every one
+    e_tab = (got - tab).abs().amax(1) / scale
+    e_fil = (got - fil).abs().amax(1) / scale
+    ok = (e_tab < 3e-2) & (e_fil < 6e-2)
+    assert ok.float().mean().item() >= 0.75, (variant, e_tab.tolist(), e_fil.tolist())
+    top2 = fil.topk(2, dim=1).values
+    decided = ok & ((top2[:, 0] - top2[:, 1]) > 2 * e_fil * scale)
+    assert (got.argmax(1)[decided] == fil.argmax(1)[decided]).all()
+    out = eng.generate([prompt[:8]], SamplingParams(max_tokens=6))[0]
+    assert len(out) == 6 and all(0 <= t < cfg.vocab for t in out)
