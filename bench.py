@@ -123,26 +123,43 @@ def engine_e2e(eng, vocab: int, prompt_len: int, K: int, W: int, world: int, dev
 
 
 def bench_qwen_next(args, sub: bool = False):
-    """Qwen3-Next-style hybrid (config 4): bs1 / bs8 device-timed decode on one GPU, 80B-parameter
-    random weights in the mixed <= 1.5 BPW recipe (random codes + Gaussian-statistics scales).
-    ``sub``: return the result as a dict (a sub-object of the default bench line) instead of
-    printing it."""
+    """Qwen3-Next-style hybrid (config 4): bs1 / bs8 device-timed decode, 80B-parameter random
+    weights in the mixed <= 1.5 BPW recipe (random codes + Gaussian-statistics scales); on N > 1
+    ranks the mixers are tensor parallel over heads and the 512 experts expert parallel
+    (parallel/ep.py). ``sub``: return the result as a dict (a sub-object of the default bench
+    line) instead of printing it."""
     import torch
+    import torch.distributed as dist
     from hawking_b200.engine.kv_cache import PagedKVCache
     from hawking_b200.models.config import preset
     from hawking_b200.models.qwen_next import QwenNextModel, random_qwen_next_weights
     from hawking_b200.utils.clocks import ClockSampler
-    dev = torch.device("cuda", 0)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    if world > 1 and not dist.is_initialized():
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
     K, W, ctx = args.steps, args.warmup, args.ctx
     cfg = preset("qwen3-next", max_ctx=max(ctx, args.e2e_ctx) + 2 * (K + W) + 64)
     if args.layers:
         cfg = cfg.with_(layers=args.layers)
     t0 = time.time()
-    w = random_qwen_next_weights(cfg, dev, seed=0)
+    tp = None
+    mcfg = cfg
+    if world > 1:
+        from hawking_b200.parallel.ep import local_qwen_next_config
+        from hawking_b200.parallel.tp import TPComm
+        w = random_qwen_next_weights(cfg, dev, seed=0, shard=(rank, world))
+        tp = TPComm(rank, world, 2 * cfg.layers, 8, cfg.hidden, dev)
+        mcfg = local_qwen_next_config(cfg, world)
+    else:
+        w = random_qwen_next_weights(cfg, dev, seed=0)
     t_load = time.time() - t0
     artifact = None
-    if args.artifact:
+    if args.artifact and world == 1:
         # through a `.gravity` artifact: written with the repo's writer, read back (every payload's
         # sha256 verified once at admission) and decoded from the loaded planes
         import shutil
@@ -165,10 +182,10 @@ def bench_qwen_next(args, sub: bool = False):
     n_full = sum(cfg.layer_is_full_attention(l) for l in range(cfg.layers))
     bs, max_seqs = 64, 8
     max_blocks = -(-cfg.max_ctx // bs)
-    kv = PagedKVCache(n_full, cfg.n_kv_heads, cfg.head_dim, max_seqs * max_blocks + 8, bs, max_seqs, max_blocks, dev,
+    kv = PagedKVCache(n_full, mcfg.n_kv_heads, cfg.head_dim, max_seqs * max_blocks + 8, bs, max_seqs, max_blocks, dev,
                       prefix_cache=False)
-    m = QwenNextModel(cfg, w, kv, max_rows=8, max_seqs=max_seqs, device=dev)
-    g = torch.Generator(device=dev).manual_seed(1)
+    m = QwenNextModel(mcfg, w, kv, max_rows=8, max_seqs=max_seqs, device=dev, tp=tp)
+    g = torch.Generator(device=dev).manual_seed(1 + rank)
     for l in range(n_full):
         kv.k[l].normal_(0, 1, generator=g)
         kv.v[l].normal_(0, 1, generator=g)
@@ -188,20 +205,34 @@ def bench_qwen_next(args, sub: bool = False):
             pos.append(ctx)
             rseq.append(kv.row(sid))
             rctx.append(ctx + 1)
+        if world > 1:  # every rank decodes the same token ids (the hidden state is replicated)
+            t = torch.tensor(ids, dtype=torch.int32, device=dev)
+            dist.broadcast(t, 0)
+            ids = t.tolist()
         m.inp.upload(ids, pos, [0] * nseq, rseq, rctx)
         for _ in range(W):
             m.graph_forward(nseq, "greedy", advance=True)
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with ClockSampler(0, period_ms=50) as cs:
+        with ClockSampler(local, period_ms=50) as cs:
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize()
             e0.record()
             for _ in range(K):
                 m.graph_forward(nseq, "greedy", advance=True)
             e1.record()
             torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
         for i in range(nseq):
             kv.drop(10 + i)
-        return e0.elapsed_time(e1) / K, cs.result
+        ms = e0.elapsed_time(e1) / K
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = t.item()
+        return ms, cs.result
 
     if args.profile_step:
         profile_one_step(m, kv, ctx)
@@ -210,12 +241,17 @@ def bench_qwen_next(args, sub: bool = False):
     launches = m.launches_per_graph
     ms8, clocks8 = timed(8)
     from hawking_b200.engine.engine import Engine
-    eng = Engine(cfg, m, kv, max_batch=max_seqs - 1, max_prefill_tokens=8)
-    e2e, ttft = engine_e2e(eng, cfg.vocab, args.e2e_ctx, K, W, 1, dev)
+    eng = Engine(mcfg, m, kv, max_batch=max_seqs - 1, max_prefill_tokens=8)
+    e2e, ttft = engine_e2e(eng, cfg.vocab, args.e2e_ctx, K, W, world, dev)
+    if tp is not None:
+        tp.check()
+        m.release_graphs()
+        tp.close()
     out = {
-        "metric": "decode tok/s bs1 (Qwen3-Next-style hybrid MoE, .gravity mixed <= 1.5 BPW), 1 GPU",
-        "value": round(1000.0 / ms1, 2), "unit": "tok/s", "n_gpus": 1, "steps": K, "warmup": W,
-        "ms_per_step": round(ms1, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "metric": "decode tok/s bs1 (Qwen3-Next-style hybrid MoE, .gravity mixed <= 1.5 BPW), %d GPU" % world,
+        "value": round(1000.0 / ms1, 2), "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": round(ms1, 4), "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
+        "vs_baseline": None,
         "dtype": "binary/ternary experts and Q4 projections (per-64 fp16 group scales) x int8 activation blocks, "
                  "fp32 accumulate and DeltaNet state, bf16 KV",
         "data": "synthetic: random codes with Gaussian-statistics group scales (80B-parameter model), random KV "
@@ -223,21 +259,26 @@ def bench_qwen_next(args, sub: bool = False):
         "config": {"model": "qwen3-next (48 layers, hidden 2048, 12 gated full-attention layers 16/2 heads hd 256, "
                             "36 gated DeltaNet layers 16k/32v heads hd 128, 512 experts top-10 + shared, FFN 512, "
                             "vocab 151936)" + (f" [LAYERS OVERRIDDEN to {cfg.layers}]" if args.layers else ""),
-                   "global_batch": 1, "seq_len": ctx, "parallelism": "tp1",
+                   "global_batch": 1, "seq_len": ctx,
+                   "parallelism": "tp1" if world == 1 else "tp%d mixers + ep%d experts" % (world, world),
                    "complete_bpw": round(complete_bpw, 3),
-                   "l2": "inputs larger than L2: %.1f GB of weights resident" % ((w.table.nbytes + w.embed.nbytes) / 1e9)},
+                   "l2": "inputs larger than L2: %.1f GB of weights resident per GPU" % ((w.table.nbytes + w.embed.nbytes) / 1e9)},
         "clocks": clocks, "e2e": e2e, "ttft_ms": ttft, "ttft_prompt": args.e2e_ctx,
         "ttft_note": "prompts prefill in 8-token runs per forward (the DeltaNet kernels walk a run token by token, state in registers); no chunked WY form",
         "gpu_launches": launches * K,
         "bs8": {"tok_s_aggregate": round(8 * 1000.0 / ms8, 1), "ms_per_step": round(ms8, 4), "clocks": clocks8},
         "weights_gb": round((w.table.nbytes + w.embed.nbytes) / 1e9, 2),
         "expert_weights_gb": round(expert_bytes / 1e9, 2), "load_s": round(t_load, 1),
-        "artifact": artifact or "in-memory weights (--artifact 0)",
+        "artifact": artifact or ("in-memory weights (--artifact 0)" if world == 1 else "in-memory shards (N > 1)"),
     }
     if sub:
         m.release_graphs()
         return out
-    print(json.dumps(out))
+    if rank == 0:
+        print(json.dumps(out))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
     return 0
 
 
@@ -794,11 +835,7 @@ def main():
         gc.collect()
         torch.cuda.empty_cache()
         barrier()
-        if world == 1:
-            out["qwen3_next"] = bench_qwen_next(fa, sub=True)
-        else:
-            out["qwen3_next"] = {"unavailable": "Qwen3-Next has no tensor/expert parallelism yet; its 1-GPU "
-                                                "numbers are in the N=1 line"}
+        out["qwen3_next"] = bench_qwen_next(fa, sub=True)
         gc.collect()
         torch.cuda.empty_cache()
     if rank == 0:

@@ -131,8 +131,13 @@ void moe_mixed_gemv(int64_t epi, const Tensor& descs, int64_t base0, int64_t bas
                     const optional<Tensor>& oq, const optional<Tensor>& od, const optional<Tensor>& os,
                     const optional<Tensor>& y, const optional<Tensor>& route_w, bool pdl, int64_t routed_pairs,
                     bool direct, int64_t e_lo, int64_t e_count, int64_t T, const optional<Tensor>& push_table,
-                    const optional<Tensor>& push_epoch) {
+                    const optional<Tensor>& push_epoch, const optional<Tensor>& shared_gate) {
   hk::MoeMixedArgs a{};
+  if (shared_gate.has_value()) {
+    TORCH_CHECK(shared_gate->is_cuda() && shared_gate->scalar_type() == at::kFloat, "moe_mixed_gemv: fp32 shared gate logits");
+    a.shared_gate = shared_gate->data_ptr<float>();
+    a.shared_gate_stride = shared_gate->dim() > 1 ? shared_gate->stride(0) : 1;
+  }
   a.e_lo = (int)e_lo;
   a.e_count = (int)e_count;
   a.T = (int)T;
@@ -427,7 +432,7 @@ void register_model_kernels(py::module_& m) {
         py::arg("route_w") = py::none(), py::arg("pdl") = false,
         py::arg("routed_pairs") = -1,
         py::arg("direct") = false, py::arg("e_lo") = 0, py::arg("e_count") = 0, py::arg("T") = 0,
-        py::arg("push_table") = py::none(), py::arg("push_epoch") = py::none());
+        py::arg("push_table") = py::none(), py::arg("push_epoch") = py::none(), py::arg("shared_gate") = py::none());
   m.def("deltanet_conv", &deltanet_conv, py::arg("qkvz"), py::arg("conv_w"), py::arg("conv_state"), py::arg("slot"),
         py::arg("kh"), py::arg("r"), py::arg("dk"), py::arg("dv"), py::arg("kc"), py::arg("eps"), py::arg("q"),
         py::arg("k"), py::arg("v"), py::arg("z"), py::arg("pdl") = false);

@@ -550,7 +550,10 @@ struct MoeMixedArgs {
   int64_t y_stride;
   const float* route_w;
   int routed_pairs;           // pairs below this are routed (token pair / k, weight route_w[pair]);
-                              // the rest are shared-expert pairs (token pair - routed_pairs, weight 1)
+                              // the rest are shared-expert pairs (token pair - routed_pairs, weight 1,
+                              // or sigmoid(shared_gate[token]) for a gated shared expert)
+  const float* shared_gate;   // per-token shared-expert gate logits (stride shared_gate_stride) or null
+  int64_t shared_gate_stride;
   int direct;                 // epi 0: read each pair's token row of xq/xd/xs (strides below)
   int64_t x_stride_q, x_stride_s;
   // expert parallelism: the table holds this rank's experts e_lo .. e_lo + e_count - 1 at

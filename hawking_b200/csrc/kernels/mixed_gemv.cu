@@ -212,6 +212,12 @@ __device__ __forceinline__ int moe_desc_index(const MoeMixedArgs& a, int e) {
   return (l >= 0 && l < a.e_count) ? l : a.e_count;
 }
 
+// Weight of sorted pair `pair` of token `tok`: its route weight, or the shared expert's gate.
+__device__ __forceinline__ float moe_pair_weight(const MoeMixedArgs& a, int pair, int tok) {
+  if (pair < a.routed_pairs) return a.route_w[pair];
+  return a.shared_gate ? 1.f / (1.f + __expf(-a.shared_gate[(int64_t)tok * a.shared_gate_stride])) : 1.f;
+}
+
 // Grid (row blocks, active experts): blockIdx.y indexes a.active (experts with >= 1 pair).
 template <int EPI>
 __global__ void __launch_bounds__(256) moe_mixed_gemv_kernel(MoeMixedArgs a) {
@@ -267,7 +273,7 @@ __global__ void __launch_bounds__(256) moe_mixed_gemv_kernel(MoeMixedArgs a) {
         const int pair = a.sorted[sp];
         const bool routed = pair < a.routed_pairs;
         const int tok = routed ? pair / a.k : pair - a.routed_pairs;
-        atomicAdd(a.y + (int64_t)tok * a.y_stride + n, (routed ? a.route_w[pair] : 1.f) * v);
+        atomicAdd(a.y + (int64_t)tok * a.y_stride + n, moe_pair_weight(a, pair, tok) * v);
       }
     }
   }
@@ -298,7 +304,7 @@ __global__ void __launch_bounds__(256) moe_mixed_combine_push_kernel(MoeMixedArg
       const int pair = a.sorted[sp];
       const bool routed = pair < a.routed_pairs;
       const int tok = routed ? pair / a.k : pair - a.routed_pairs;
-      if (lane == tok) acc += (routed ? a.route_w[pair] : 1.f) * v;
+      if (lane == tok) acc += moe_pair_weight(a, pair, tok) * v;
     }
   }
   pdl_launch();

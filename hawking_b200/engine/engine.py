@@ -141,11 +141,12 @@ class Engine:
     @staticmethod
     def build_qwen_next(cfg: ModelConfig, weights, device="cuda", max_batch: int = 8, max_ctx: Optional[int] = None,
                         block_size: int = 64, num_blocks: Optional[int] = None, kv_fraction: float = 0.5,
-                        policy: int = 0):
+                        policy: int = 0, tp=None):
         """Engine around the hybrid DeltaNet / gated-attention model: paged KV for the full-
         attention layers, one recurrent-state slot per block-table row (reset when a sequence
         starts), no prefix reuse (a cached prefix would not restore the recurrent state), and
-        one row per sequence per forward (the recurrence is sequential)."""
+        one row per sequence per forward (the recurrence is sequential). ``tp``: ``cfg`` and
+        ``weights`` are this rank's tensor / expert-parallel shard."""
         from ..models.qwen_next import QwenNextModel
         max_ctx = max_ctx or cfg.max_ctx
         max_blocks = -(-max_ctx // block_size)
@@ -156,7 +157,7 @@ class Engine:
             num_blocks = min(int(free * kv_fraction // bpb), (max_batch + 1) * max_blocks + 16)
         kv = PagedKVCache(max(1, n_full), cfg.n_kv_heads, cfg.head_dim, num_blocks, block_size, max_batch + 1,
                           max_blocks, device, prefix_cache=False)
-        model = QwenNextModel(cfg, weights, kv, max_rows=8, max_seqs=max_batch + 1, device=device)
+        model = QwenNextModel(cfg, weights, kv, max_rows=8, max_seqs=max_batch + 1, device=device, tp=tp)
         return Engine(cfg, model, kv, max_batch=max_batch, max_prefill_tokens=8 * max_batch, policy=policy)
 
     @staticmethod

@@ -408,6 +408,7 @@ def engine_buffers(model, R: int):
     model.temperature = torch.zeros(R, device=dev)
     model.top_k = torch.zeros(R, dtype=torch.int32, device=dev)
     model.top_p = torch.ones(R, device=dev)
+    model.rep_penalty = torch.ones(R, device=dev)
     model.uniforms = torch.zeros(R, device=dev)
 
 

@@ -29,7 +29,8 @@ import torch
 from .. import ops
 from .._ext import kernels
 from ..ops import Q8Act, QWeight
-from ..ops.mixed import BINARY, UNIFORM, MixedTable, MixedWeight, mixed_gemv, mixed_gemv_swiglu
+from ..ops.mixed import (BINARY, UNIFORM, MixedTable, MixedWeight, mixed_gemv, mixed_gemv_push,
+                         mixed_gemv_swiglu)
 from .config import ModelConfig
 
 
@@ -47,6 +48,7 @@ class QNLayer:
     ssm_norm: Optional[torch.Tensor] = None
     router: Optional[torch.Tensor] = None               # fp32 [E, H]
     shared_gate: Optional[torch.Tensor] = None          # fp32 [1, H]
+    shared_here: bool = True                            # expert parallel: this rank runs the shared expert
 
 
 @dataclass
@@ -56,6 +58,8 @@ class QNWeights:
     out_norm: torch.Tensor
     layers: List[QNLayer]
     lm_head: int
+    e_lo: int = 0                       # expert parallel: this rank's routed experts are
+    e_count: int = 0                    # e_lo .. e_lo + e_count - 1 (0: all of them)
 
     @property
     def nbytes(self) -> int:
@@ -78,14 +82,25 @@ def expert_codec(rng: random.Random, ternary_fraction: float):
 
 
 def random_qwen_next_weights(cfg: ModelConfig, device, seed: int = 0, std: float = 0.02,
-                             ternary_fraction: float = 0.10, group: int = 64, materialise: bool = False) -> QNWeights:
+                             ternary_fraction: float = 0.10, group: int = 64, materialise: bool = False,
+                             shard: Optional[tuple] = None) -> QNWeights:
     """Random-init weights in the benchmark's mixed recipe. ``materialise`` draws Gaussian weights
     and encodes them (small configs / tests); otherwise random codes and Gaussian-statistics
-    scales are written directly (the 80B benchmark model)."""
+    scales are written directly (the 80B benchmark model). ``shard`` = (rank, world): only that
+    rank's tensor / expert-parallel shard, in its shapes (``parallel.ep.local_qwen_next_config``);
+    the replicated router and shared-expert gate agree on every rank."""
     g = torch.Generator(device=device)
     g.manual_seed(seed)
+    gs = torch.Generator(device=device)
+    gs.manual_seed(seed + 7919)  # replicated tensors
     rng = random.Random(seed)
-    H, E, F, Fs, V = cfg.hidden, cfg.n_experts, cfg.expert_ffn, cfg.shared_ffn, cfg.vocab
+    rank, world = shard or (0, 1)
+    E_all = cfg.n_experts
+    if world > 1:
+        from ..parallel.ep import local_qwen_next_config
+        g.manual_seed(seed * 1009 + 1 + rank)
+        cfg = local_qwen_next_config(cfg, world)
+    H, E, F, Fs, V = cfg.hidden, cfg.n_experts // world, cfg.expert_ffn, cfg.shared_ffn, cfg.vocab // world
     nh, nkv, hd = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
     dm = dims(cfg)
     ws: List[MixedWeight] = []
@@ -120,30 +135,38 @@ def random_qwen_next_weights(cfg: ModelConfig, device, seed: int = 0, std: float
             L.a_log = torch.log(torch.rand(dm["vh"], generator=g, device=device) * 15 + 1)
             L.dt_bias = torch.randn(dm["vh"], generator=g, device=device) * 0.5
             L.ssm_norm = ones(dm["dv"])
-        L.router = torch.randn(E, H, generator=g, device=device) * std
-        L.shared_gate = torch.randn(1, H, generator=g, device=device) * std
-        for m in ("eg", "eu"):
+        L.router = torch.randn(E_all, H, generator=gs if world > 1 else g, device=device) * std
+        L.shared_gate = torch.randn(1, H, generator=gs if world > 1 else g, device=device) * std
+        L.shared_here = (l % world) == rank
+        for m, sm in (("eg", "sg"), ("eu", "su"), ("ed", "sd")):
+            n, k = (F, H) if m != "ed" else (H, F)
             L.idx[m] = len(ws)
             for _ in range(E):
-                add(F, H, *expert_codec(rng, ternary_fraction))
-        L.idx["ed"] = len(ws)
-        for _ in range(E):
-            add(H, F, *expert_codec(rng, ternary_fraction))
-        L.idx["sg"] = add(Fs, H, UNIFORM, 4)
-        L.idx["su"] = add(Fs, H, UNIFORM, 4)
-        L.idx["sd"] = add(H, Fs, UNIFORM, 4)
+                add(n, k, *expert_codec(rng, ternary_fraction))
+            if world > 1 and L.shared_here:  # the shared expert follows this rank's routed experts
+                L.idx[sm] = add(Fs if m != "ed" else H, H if m != "ed" else Fs, UNIFORM, 4)
+        if world == 1:
+            L.idx["sg"] = add(Fs, H, UNIFORM, 4)
+            L.idx["su"] = add(Fs, H, UNIFORM, 4)
+            L.idx["sd"] = add(H, Fs, UNIFORM, 4)
         layers.append(L)
     head = add(V, H, UNIFORM, 4)
-    emb = QWeight.quantize(torch.randn(V, H, generator=g, device=device) * std, 1)  # F16 table
+    emb = QWeight.quantize(torch.randn(cfg.vocab, H, generator=gs if world > 1 else g, device=device) * std, 1)
     torch.cuda.synchronize(device)
-    return QNWeights(MixedTable(ws), emb, ones(H), layers, head)
+    return QNWeights(MixedTable(ws), emb, ones(H), layers, head, e_lo=rank * E if world > 1 else 0,
+                     e_count=E if world > 1 else 0)
 
 
 class QwenNextModel:
     """Decode forward over static buffers (rows <= 8, one token per row)."""
 
-    def __init__(self, cfg: ModelConfig, w: QNWeights, kv, max_rows: int = 8, max_seqs: int = 8, device="cuda"):
+    def __init__(self, cfg: ModelConfig, w: QNWeights, kv, max_rows: int = 8, max_seqs: int = 8, device="cuda",
+                 tp=None):
+        """With ``tp`` (parallel.tp.TPComm), ``cfg`` and ``w`` are this rank's shard
+        (``parallel.ep.local_qwen_next_config`` / ``shard_qwen_next_weights``): two push all-reduce
+        sites per layer (mixer output, expert combine), each consumed by the next RMSNorm."""
         self.cfg, self.w, self.kv, self.dev = cfg, w, kv, torch.device(device)
+        self.tp = tp
         self.max_rows = R = min(max_rows, 8)
         dev = self.dev
         H, nh, nkv, hd = cfg.hidden, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
@@ -179,17 +202,23 @@ class QwenNextModel:
         self.sglog = torch.zeros(R, 1, device=dev)
         self.ids = torch.zeros(R, k, dtype=torch.int32, device=dev)
         self.rw = torch.zeros(R, k, device=dev)
-        self.counts = torch.zeros(E, dtype=torch.int32, device=dev)
-        self.offsets = torch.zeros(E, dtype=torch.int32, device=dev)
-        self.sorted = torch.zeros(R * k, dtype=torch.int32, device=dev)
-        self.active = torch.zeros(E, dtype=torch.int32, device=dev)
+        self.counts = torch.zeros(E + 1, dtype=torch.int32, device=dev)
+        self.offsets = torch.zeros(E + 1, dtype=torch.int32, device=dev)
+        self.sorted = torch.zeros(R * k + R, dtype=torch.int32, device=dev)
+        self.active = torch.zeros(E + 1, dtype=torch.int32, device=dev)
         self.n_active = torch.zeros(1, dtype=torch.int32, device=dev)
         self.route_counter = torch.zeros(1, dtype=torch.int32, device=dev)
         self.fused_route = cfg.hidden % 512 == 0 and E < 1024
         self.gx = Q8Act(R * k, H, dev)
-        self.hx = Q8Act(R * k, F, dev)
+        self.hx = Q8Act(R * k + R, F, dev)
         self.hs = Q8Act(R, Fs, dev)
-        self.logits = torch.zeros(R, cfg.vocab, device=dev)
+        # this rank's vocabulary slice under tensor parallelism
+        self.logits = torch.zeros(R, w.table.weights[w.lm_head].N, device=dev)
+        if tp is not None:
+            if not self.fused_route:
+                raise ValueError("qwen3next tensor parallelism needs the fused routing kernel (hidden % 512 == 0)")
+            self.x2 = torch.zeros(R, H, device=dev)  # second residual buffer of the push all-reduce
+            self.argmax_slots = torch.zeros(R, ops.ARGMAX_SLOTS, dtype=torch.int64, device=dev)
         self.next_ids = torch.zeros(R, dtype=torch.int32, device=dev)
         self.rope = ops.rope_table(cfg.max_ctx, cfg.rope_dim, cfg.rope_theta, None, dev)
         self.scale = 1.0 / math.sqrt(hd)
@@ -216,7 +245,7 @@ class QwenNextModel:
             s *= 2
         return s
 
-    def _full(self, l, L, rows):
+    def _full(self, l, L, rows, site: int = -1):
         cfg, w, kv, inp = self.cfg, self.w, self.kv, self.inp
         nh, nkv, hd = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
         t, xa = w.table, self.xa.view(rows)
@@ -235,9 +264,12 @@ class QwenNextModel:
         ops.launches.add()
         kernels().sigmoid_gate_q8(self.att[:rows], self.gate[:rows], self.attq.q[:rows], self.attq.d[:rows],
                                   self.attq.s[:rows], ops.PDL)
-        mixed_gemv(t, L.idx["o"], self.attq.view(rows), self.x[:rows], residual=True)
+        if site >= 0:
+            mixed_gemv_push(t, L.idx["o"], self.attq.view(rows), self.tp, site)
+        else:
+            mixed_gemv(t, L.idx["o"], self.attq.view(rows), self.x[:rows], residual=True)
 
-    def _linear(self, l, L, rows):
+    def _linear(self, l, L, rows, site: int = -1):
         cfg, t, dm, inp = self.cfg, self.w.table, self.dm, self.inp
         xa = self.xa.view(rows)
         li = self.lin_index[l]
@@ -251,7 +283,35 @@ class QwenNextModel:
                                      self.dv_[:rows], self.dz[:rows], self.ba[:rows], L.a_log, L.dt_bias, dm["r"],
                                      dm["dk"], dm["dv"], L.ssm_norm, cfg.eps, None, self.dout.q[:rows],
                                      self.dout.d[:rows], self.dout.s[:rows], ops.PDL)
-        mixed_gemv(t, L.idx["out"], self.dout.view(rows), self.x[:rows], residual=True)
+        if site >= 0:
+            mixed_gemv_push(t, L.idx["out"], self.dout.view(rows), self.tp, site)
+        else:
+            mixed_gemv(t, L.idx["out"], self.dout.view(rows), self.x[:rows], residual=True)
+
+    def _moe_tp(self, L, rows, site: int):
+        """Expert-parallel MoE: routing replicated (every rank scores all experts from the same
+        hidden state), this rank's experts plus, on rank l mod N, the shared expert as one more
+        pair per token weighted by sigmoid(shared-gate logit); the combine pushes each token's sum
+        into every rank's receive region of ``site``."""
+        cfg, t, tp, K = self.cfg, self.w.table, self.tp, kernels()
+        k, H, F = cfg.top_k, cfg.hidden, cfg.expert_ffn
+        xa = self.xa.view(rows)
+        ne, e_lo = self.w.e_count, self.w.e_lo
+        fold = L.shared_here
+        ops.router_logits(L.shared_gate, xa, self.sglog[:rows])
+        ops.moe_route(L.router, xa, k, 0, None, 1, 1, cfg.norm_topk, 1.0, self.rlog[:rows], self.ids[:rows],
+                      self.rw[:rows], self.counts, self.offsets, self.sorted, self.active, self.n_active, fold,
+                      self.route_counter, e_lo=e_lo, e_hi=e_lo + ne)
+        ops.launches.add(2)
+        na = min(ne, rows * k) + (1 if fold else 0)
+        ep = dict(e_lo=e_lo, e_count=ne)
+        K.moe_mixed_gemv(0, t.descs, L.idx["eg"], L.idx["eu"], F, H, k, self.counts, self.offsets, self.sorted,
+                         self.active, self.n_active, na, xa.q, xa.d, xa.s, self.hx.q, self.hx.d, self.hx.s, None, None,
+                         ops.PDL, rows * k, True, **ep)
+        K.moe_mixed_gemv(2, t.descs, L.idx["ed"], L.idx["ed"], H, F, k, self.counts, self.offsets, self.sorted,
+                         self.active, self.n_active, na, self.hx.q, self.hx.d, self.hx.s, None, None, None, None,
+                         self.rw[:rows].reshape(-1), ops.PDL, rows * k, T=rows, push_table=tp.push_recv[site],
+                         push_epoch=tp.epoch, shared_gate=self.sglog[:rows], **ep)
 
     def _moe(self, L, rows):
         cfg, t = self.cfg, self.w.table
@@ -287,8 +347,50 @@ class QwenNextModel:
         """``n_logits`` (engine): > 0 moves the logits / greedy ids of ``logit_rows[:n_logits]`` to
         the first rows. Rows must belong to distinct sequences (``serial_rows``)."""
         from .deepseek import compact_logit_rows
-        self._forward(rows, sample, advance)
+        if self.tp is not None:
+            self._forward_tp(rows, sample, advance)
+        else:
+            self._forward(rows, sample, advance)
         compact_logit_rows(self, n_logits)
+
+    def _forward_tp(self, rows: int, sample: str, advance: bool):
+        cfg, w, inp, tp = self.cfg, self.w, self.inp, self.tp
+        ops.tp_begin(tp)
+        xa_res, xb_res = self.x[:rows], self.x2[:rows]
+        ops.embed(w.embed, inp.ids[:rows], xa_res)
+        ops.rmsnorm_q8(xa_res, w.layers[0].attn_norm, cfg.eps, self.xa.view(rows))
+        for l, L in enumerate(w.layers):
+            if L.full:
+                self._full(l, L, rows, site=2 * l)
+            else:
+                self._linear(l, L, rows, site=2 * l)
+            ops.tp_allreduce_rmsnorm_q8(tp, 2 * l, xa_res, xb_res, L.post_norm, cfg.eps, self.xa.view(rows))
+            self._moe_tp(L, rows, 2 * l + 1)
+            nxt = w.layers[l + 1].attn_norm if l + 1 < len(w.layers) else w.out_norm
+            ops.tp_allreduce_rmsnorm_q8(tp, 2 * l + 1, xb_res, xa_res, nxt, cfg.eps, self.xa.view(rows))
+        head = w.table.weights[w.lm_head]
+        if sample == "greedy":
+            mixed_gemv(w.table, w.lm_head, self.xa.view(rows), self.logits[:rows],
+                       argmax_slots=self.argmax_slots[:rows], argmax_offset=tp.rank * head.N)
+            ops.tp_argmax(tp, self.argmax_slots, rows, self.next_ids)
+        elif sample == "none":
+            mixed_gemv(w.table, w.lm_head, self.xa.view(rows), self.logits[:rows])
+        else:  # vocabulary-parallel logits, gathered; every rank draws the same token
+            mixed_gemv(w.table, w.lm_head, self.xa.view(rows), self.logits[:rows])
+            ops.sample(self.gathered_logits(rows), self.temperature[:rows], self.top_k[:rows], self.top_p[:rows],
+                       self.rep_penalty[:rows], None, self.uniforms[:rows], self.next_ids[:rows])
+        if advance:
+            ops.advance(inp.ids, self.next_ids, inp.positions, inp.row_ctx, rows)
+
+    def gathered_logits(self, nl: int) -> torch.Tensor:
+        """Logits of the first ``nl`` rows over the whole vocabulary (the ranks' slices gathered
+        under tensor parallelism; a collective every rank calls for the same rows)."""
+        if self.tp is None:
+            return self.logits[:nl]
+        from ..parallel.tp import gather_vocab_logits
+        if getattr(self, "_tp_full", None) is None:
+            self._tp_full = torch.zeros(self.logits.shape[0], self.logits.shape[1] * self.tp.world, device=self.dev)
+        return gather_vocab_logits(self.tp, self.logits[:nl], self._tp_full)
 
     def _forward(self, rows: int, sample: str = "greedy", advance: bool = False):
         cfg, w, inp = self.cfg, self.w, self.inp
@@ -319,7 +421,7 @@ class QwenNextModel:
         r = kv.row(seq_id)
         if start_pos == 0:
             self.reset_state(r)
-        out = torch.empty(n, self.cfg.vocab, device=self.dev)
+        out = torch.empty(n, self.logits.shape[1], device=self.dev)  # this rank's vocabulary slice under TP
         for c0 in range(0, n, self.max_rows):
             c1 = min(n, c0 + self.max_rows)
             p0 = start_pos + c0

@@ -1,4 +1,5 @@
-"""Expert parallelism (with tensor-parallel attention) for the DeepSeek-style MLA + MoE decoder.
+"""Expert parallelism (with tensor-parallel attention) for the DeepSeek-style MLA + MoE decoder and the
+Qwen3-Next hybrid.
 
 Plan for rank r of N GPUs of one node:
 
@@ -146,3 +147,94 @@ def random_deepseek_weights_ep(cfg: ModelConfig, rank: int, world: int, device, 
     emb = QWeight.quantize(torch.randn(cfg.vocab, H, generator=gs, device=device) * std, 1)
     torch.cuda.synchronize(device)
     return DSWeights(MixedTable(ws), emb, ones(H), layers, head, e_lo=rank * ne, e_count=ne)
+
+
+# ---- Qwen3-Next hybrid: tensor-parallel mixers, expert-parallel MoE --------------------------------
+# Rank r of N: full-attention query / gate heads split (n_heads / N each); key / value heads split
+# when N <= n_kv_heads, otherwise each rank computes the one KV head its query heads read (KV
+# replicated across that head's ranks); DeltaNet key heads split (with their value heads, the
+# per-head q | k | v | z rows of the fused projection, the b | a rows, the conv channels and the
+# decay parameters); output projections row-parallel (column slices) pushed into the all-reduce;
+# routed experts whole on their rank, the sigmoid-gated shared expert on rank l mod N (folded into
+# that rank's expert launches with the gate as its pair weight); LM head split by vocabulary row.
+
+def local_qwen_next_config(cfg: ModelConfig, world: int) -> ModelConfig:
+    nh, nkv, kh = cfg.n_heads, cfg.n_kv_heads, cfg.linear_k_heads
+    if nh % world or kh % world or cfg.n_experts % world or cfg.vocab % world:
+        raise ValueError(f"qwen3next over {world} ranks: heads {nh}, key heads {kh}, experts {cfg.n_experts} and "
+                         f"vocab {cfg.vocab} must divide")
+    if cfg.shared_ffn != cfg.expert_ffn:
+        raise ValueError("qwen3next expert parallelism folds the shared expert into the expert launches: "
+                         "shared FFN width must equal the experts'")
+    lnh = nh // world
+    if world <= nkv:
+        if nkv % world:
+            raise ValueError(f"{nkv} KV heads do not split over {world} ranks")
+        lnkv = nkv // world
+    else:
+        if (nh // nkv) % lnh:
+            raise ValueError("a rank's query heads must read one KV head")
+        lnkv = 1
+    lkh = kh // world
+    return cfg.with_(n_heads=lnh, n_kv_heads=lnkv, linear_k_heads=lkh,
+                     linear_v_heads=cfg.linear_v_heads // world)
+
+
+def _kv_head0(cfg: ModelConfig, rank: int, world: int) -> int:
+    lnh = cfg.n_heads // world
+    if world <= cfg.n_kv_heads:
+        return rank * (cfg.n_kv_heads // world)
+    return rank * lnh // (cfg.n_heads // cfg.n_kv_heads)
+
+
+def shard_qwen_next_weights(w, cfg: ModelConfig, rank: int, world: int):
+    """Rank ``rank``'s shard of full QNWeights (``cfg``: the full config)."""
+    from ..models.qwen_next import QNLayer, QNWeights, dims
+    lc = local_qwen_next_config(cfg, world)
+    W = w.table.weights
+    hd, lnh, lnkv = cfg.head_dim, lc.n_heads, lc.n_kv_heads
+    h0, kv0 = rank * lnh, _kv_head0(cfg, rank, world)
+    dm = dims(cfg)
+    dk, rv, r = dm["dk"], dm["r"] * dm["dv"], dm["r"]
+    grp = 2 * dk + 2 * rv
+    lkh = lc.linear_k_heads
+    k0 = rank * lkh
+    KE = cfg.linear_k_heads * dk
+    E, ne = cfg.n_experts, cfg.n_experts // world
+    e_lo = rank * ne
+    ws: List[MixedWeight] = []
+
+    def put(mw: MixedWeight) -> int:
+        ws.append(mw)
+        return len(ws) - 1
+
+    layers = []
+    for l, L in enumerate(w.layers):
+        nl = QNLayer(L.full, L.attn_norm, L.post_norm, q_norm=L.q_norm, k_norm=L.k_norm, ssm_norm=L.ssm_norm,
+                     router=L.router, shared_gate=L.shared_gate)
+        if L.full:
+            nl.idx["q"] = put(W[L.idx["q"]].rows(h0 * hd, lnh * hd).contiguous())
+            nl.idx["g"] = put(W[L.idx["g"]].rows(h0 * hd, lnh * hd).contiguous())
+            nl.idx["k"] = put(W[L.idx["k"]].rows(kv0 * hd, lnkv * hd).contiguous())
+            nl.idx["v"] = put(W[L.idx["v"]].rows(kv0 * hd, lnkv * hd).contiguous())
+            nl.idx["o"] = put(W[L.idx["o"]].cols(h0 * hd, (h0 + lnh) * hd))
+        else:
+            nl.idx["qkvz"] = put(W[L.idx["qkvz"]].rows(k0 * grp, lkh * grp).contiguous())
+            nl.idx["ba"] = put(W[L.idx["ba"]].rows(k0 * 2 * r, lkh * 2 * r).contiguous())
+            nl.idx["out"] = put(W[L.idx["out"]].cols(k0 * rv, (k0 + lkh) * rv))
+            cw = L.conv_w
+            nl.conv_w = torch.cat([cw[k0 * dk:(k0 + lkh) * dk], cw[KE + k0 * dk:KE + (k0 + lkh) * dk],
+                                   cw[2 * KE + k0 * rv:2 * KE + (k0 + lkh) * rv]]).contiguous()
+            nl.a_log = L.a_log[k0 * r:(k0 + lkh) * r].contiguous()
+            nl.dt_bias = L.dt_bias[k0 * r:(k0 + lkh) * r].contiguous()
+        nl.shared_here = (l % world) == rank
+        for m, sm in (("eg", "sg"), ("eu", "su"), ("ed", "sd")):
+            nl.idx[m] = len(ws)
+            for e in range(e_lo, e_lo + ne):
+                put(W[L.idx[m] + e])
+            if nl.shared_here:  # the shared expert follows this rank's routed experts
+                nl.idx[sm] = put(W[L.idx[sm]])
+        layers.append(nl)
+    V = cfg.vocab // world
+    head = put(W[w.lm_head].rows(rank * V, V).contiguous())
+    return QNWeights(MixedTable(ws), w.embed, w.out_norm, layers, head, e_lo=e_lo, e_count=ne)

@@ -201,11 +201,17 @@ def preset_engine(preset: str, layers: int = 0, max_batch: int = 8, max_ctx=None
             eng = Engine.build_deepseek(cfg, random_deepseek_weights(cfg, device), device=device, max_batch=max_batch,
                                         policy=policy)
     elif cfg.arch == "qwen3next":
-        if tp_world > 1:
-            raise ValueError("qwen3-next serves on one GPU (no tensor / expert parallelism yet)")
         from ..models.qwen_next import random_qwen_next_weights
-        eng = Engine.build_qwen_next(cfg, random_qwen_next_weights(cfg, device), device=device, max_batch=max_batch,
-                                     policy=policy)
+        if tp_world > 1:
+            from ..parallel.ep import local_qwen_next_config
+            from ..parallel.tp import TPComm
+            tp = TPComm(tp_rank, tp_world, 2 * cfg.layers, 8, cfg.hidden, dev)
+            eng = Engine.build_qwen_next(local_qwen_next_config(cfg, tp_world),
+                                         random_qwen_next_weights(cfg, dev, shard=(tp_rank, tp_world)), device=device,
+                                         max_batch=max_batch, policy=policy, tp=tp)
+        else:
+            eng = Engine.build_qwen_next(cfg, random_qwen_next_weights(cfg, device), device=device,
+                                         max_batch=max_batch, policy=policy)
     elif tp_world > 1:
         from ..parallel.tp import TPComm, local_config, random_llama_weights_tp
         tp = TPComm(tp_rank, tp_world, 2 * cfg.layers, 8, cfg.hidden, dev)

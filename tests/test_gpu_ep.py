@@ -79,3 +79,69 @@ def test_ep2_deepseek_matches_single_gpu(tmp_path):
     assert r["ids"][0] == r["ids"][1] == r["tp_argmax"], r  # vocabulary-parallel greedy is exact
     assert sum(a == b for a, b in zip(r["ids"][0], r["ref_ids"])) >= 2, r
     assert r["status"] == 0
+
+
+def _worker_qn(rank, world, port, out_path):
+    """Qwen3-Next hybrid over 2 ranks: mixers tensor parallel, experts expert parallel, the gated
+    shared expert folded into one rank's expert launches; logits and greedy ids vs 1 GPU."""
+    import datetime
+
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        from hawking_b200.engine.kv_cache import PagedKVCache
+        from hawking_b200.models.qwen_next import QwenNextModel, random_qwen_next_weights
+        from hawking_b200.parallel.ep import local_qwen_next_config, shard_qwen_next_weights
+        from hawking_b200.parallel.tp import TPComm
+        from test_gpu_qwen_next import tiny_cfg
+        cfg = tiny_cfg().with_(hidden=512)
+        w = random_qwen_next_weights(cfg, dev, seed=4, materialise=True, std=0.05)  # identical on every rank
+        n_full = sum(cfg.layer_is_full_attention(l) for l in range(cfg.layers))
+        lc = local_qwen_next_config(cfg, world)
+        tp = TPComm(rank, world, 2 * cfg.layers, 8, cfg.hidden, dev)
+        kv = PagedKVCache(n_full, lc.n_kv_heads, cfg.head_dim, 32, 16, 2, 16, dev)
+        m = QwenNextModel(lc, shard_qwen_next_weights(w, cfg, rank, world), kv, max_rows=8, max_seqs=3, device=dev,
+                          tp=tp)
+        toks = [5, 77, 300, 12, 9, 401, 256, 3, 44, 100, 7]
+        local = m.forward_tokens(toks, seq_id=1).contiguous()
+        ids = m.next_ids[: len(toks) - 8].clone()
+        parts = [torch.empty_like(local) for _ in range(world)]
+        dist.all_gather(parts, local)
+        full = torch.cat(parts, 1)
+        all_ids = [torch.empty_like(ids) for _ in range(world)]
+        dist.all_gather(all_ids, ids)
+        tp.check()
+        if rank == 0:
+            kv1 = PagedKVCache(n_full, cfg.n_kv_heads, cfg.head_dim, 32, 16, 2, 16, dev)
+            ref_m = QwenNextModel(cfg, w, kv1, max_rows=8, max_seqs=3, device=dev)
+            ref = ref_m.forward_tokens(toks, seq_id=1)
+            err = float((full - ref).abs().max() / ref.abs().max())
+            torch.save({"err": err, "ids": [t.tolist() for t in all_ids], "tp_argmax": full[8:].argmax(1).tolist(),
+                        "ref_ids": ref[8:].argmax(1).tolist(), "status": int(m.status.item()) if hasattr(m, "status")
+                        else 0}, out_path)
+        torch.cuda.synchronize()
+        m.release_graphs()
+        tp.close()
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep2_qwen_next_matches_single_gpu(tmp_path):
+    import sys
+
+    import torch.multiprocessing as mp
+    sys.path.insert(0, os.path.dirname(__file__))
+    out = str(tmp_path / "qn.pt")
+    mp.spawn(_worker_qn, args=(2, _free_port(), out), nprocs=2, join=True)
+    r = torch.load(out)
+    assert r["err"] < 0.03, r
+    assert r["ids"][0] == r["ids"][1] == r["tp_argmax"], r
+    assert sum(a == b for a, b in zip(r["ids"][0], r["ref_ids"])) >= 2, r
