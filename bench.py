@@ -184,7 +184,7 @@ def bench_qwen_next(args, sub: bool = False):
     max_blocks = -(-cfg.max_ctx // bs)
     kv = PagedKVCache(n_full, mcfg.n_kv_heads, cfg.head_dim, max_seqs * max_blocks + 8, bs, max_seqs, max_blocks, dev,
                       prefix_cache=False)
-    m = QwenNextModel(mcfg, w, kv, max_rows=8, max_seqs=max_seqs, device=dev, tp=tp)
+    m = QwenNextModel(mcfg, w, kv, max_rows=512 if tp is None else 8, max_seqs=max_seqs, device=dev, tp=tp)
     g = torch.Generator(device=dev).manual_seed(1 + rank)
     for l in range(n_full):
         kv.k[l].normal_(0, 1, generator=g)
@@ -241,7 +241,7 @@ def bench_qwen_next(args, sub: bool = False):
     launches = m.launches_per_graph
     ms8, clocks8 = timed(8)
     from hawking_b200.engine.engine import Engine
-    eng = Engine(mcfg, m, kv, max_batch=max_seqs - 1, max_prefill_tokens=8)
+    eng = Engine(mcfg, m, kv, max_batch=max_seqs - 1, max_prefill_tokens=m.row_limit)
     e2e, ttft = engine_e2e(eng, cfg.vocab, args.e2e_ctx, K, W, world, dev)
     if tp is not None:
         tp.check()
@@ -264,7 +264,7 @@ def bench_qwen_next(args, sub: bool = False):
                    "complete_bpw": round(complete_bpw, 3),
                    "l2": "inputs larger than L2: %.1f GB of weights resident per GPU" % ((w.table.nbytes + w.embed.nbytes) / 1e9)},
         "clocks": clocks, "e2e": e2e, "ttft_ms": ttft, "ttft_prompt": args.e2e_ctx,
-        "ttft_note": "prompts prefill in 8-token runs per forward (the DeltaNet kernels walk a run token by token, state in registers); no chunked WY form",
+        "ttft_note": "prompts prefill in forwards of up to %d rows (the DeltaNet kernels walk a run token by token, state in registers; no chunked WY form)" % m.row_limit,
         "gpu_launches": launches * K,
         "bs8": {"tok_s_aggregate": round(8 * 1000.0 / ms8, 1), "ms_per_step": round(ms8, 4), "clocks": clocks8},
         "weights_gb": round((w.table.nbytes + w.embed.nbytes) / 1e9, 2),
@@ -336,7 +336,7 @@ def bench_deepseek(args, sub: bool = False):
     bs, max_seqs = 64, 8
     max_blocks = -(-cfg.max_ctx // bs)
     kv = LatentCache(cfg.layers, max_seqs * max_blocks + 8, bs, max_seqs, max_blocks, dev)
-    m = DeepSeekModel(mcfg, w, kv, max_rows=8, device=dev, tp=tp)
+    m = DeepSeekModel(mcfg, w, kv, max_rows=512 if tp is None else 8, device=dev, tp=tp)
     g = torch.Generator(device=dev).manual_seed(1)
     for lat in kv.latent:
         lat.normal_(0, 1, generator=g)
@@ -387,7 +387,7 @@ def bench_deepseek(args, sub: bool = False):
     launches = m.launches_per_graph
     ms8, clocks8 = timed(8)
     from hawking_b200.engine.engine import Engine
-    eng = Engine(mcfg, m, kv, max_batch=8, max_prefill_tokens=8)
+    eng = Engine(mcfg, m, kv, max_batch=8, max_prefill_tokens=m.row_limit)
     e2e, ttft = engine_e2e(eng, cfg.vocab, args.e2e_ctx, K, W, world, dev)
     if tp is not None:
         tp.check()

@@ -22,6 +22,8 @@
 // flash decode), oracle crates/hawking-core/src/attn.rs:23 (mha_decode_step).
 #include <cooperative_groups.h>
 
+#include <cstdlib>
+
 #include <mutex>
 #include <unordered_map>
 
@@ -46,13 +48,19 @@ template <int NC> struct Cfg {
   static constexpr int kConsumers = NC;
   static constexpr int kThreads = (NC + 1) * 32;  // + one producer warp
 };
-constexpr int kStages = 4;                    // ring stages (one KV block each)
+constexpr int kStages = 4;                    // ring stages at most (one KV block each)
+// Stages a launch uses (TcArgs.stages): 4, or 2 with HK_ATTN_STAGES=2 for blocks of 32 / 64 tokens
+// (a smaller ring leaves shared memory for the neighbouring kernels of the decode chain to be
+// resident at their programmatic launch). Parity soundness with 2 stages: at 64 tokens per block
+// every consumer visits every block; at 32 a consumer's blocks step by 2, all in one stage.
+// Blocks of 16 keep 4 stages (a consumer's blocks step by 4).
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct TcArgs {
   const float* q;          // [R, nh, HD] fp32 (roped)
   const __nv_bfloat16* k_base;  // caches as raw pointers (speculative L2 prefetch)
   const __nv_bfloat16* v_base;
+  int stages;              // ring stages used (2 or 4)
   int64_t cache_rows;
   int table_rows;
   const int* block_tables;
@@ -82,6 +90,7 @@ __global__ void __launch_bounds__(Cfg<NC>::kThreads, 1)
   const int kvh = blockIdx.y, r = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bs = a.block_size;
+  const int ns = a.stages;  // ring stages
   const int stage_bytes = 2 * bs * HD * 2;  // K and V of one block
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte aligned stage area (the 128-byte swizzle repeats every 8 rows of 128 bytes)
@@ -93,7 +102,7 @@ __global__ void __launch_bounds__(Cfg<NC>::kThreads, 1)
   for (int i = threadIdx.x; i < 16 * HD; i += kThreads) (&s_o[0][0])[i] = 0.f;
   if (threadIdx.x < 16) s_l[threadIdx.x] = 0.f;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kStages; ++i) {
+    for (int i = 0; i < ns; ++i) {
       sm100::mbar_init(&full[i], 1);
       sm100::mbar_init(&empty[i], (uint32_t)(a.block_size / 16));  // one arrival per 16-token unit
     }
@@ -144,8 +153,8 @@ __global__ void __launch_bounds__(Cfg<NC>::kThreads, 1)
     if (lane == 0) {
       int issued = 0;
       for (int i = 0; i < nb && ok; ++i) {
-        const int st = i % kStages;
-        if (i >= kStages && !sm100::mbar_wait(&empty[st], (uint32_t)(((i / kStages) - 1) & 1), a.status)) {
+        const int st = i % ns;
+        if (i >= ns && !sm100::mbar_wait(&empty[st], (uint32_t)(((i / ns) - 1) & 1), a.status)) {
           ok = false;
           break;
         }
@@ -160,8 +169,8 @@ __global__ void __launch_bounds__(Cfg<NC>::kThreads, 1)
         }
       }
       // unwinding or done: every issued copy must land before the CTA may exit
-      for (int i = max(0, issued - kStages); i < issued; ++i)
-        sm100::mbar_wait(&full[i % kStages], (uint32_t)((i / kStages) & 1), nullptr, 1u << 22);
+      for (int i = max(0, issued - ns); i < issued; ++i)
+        sm100::mbar_wait(&full[i % ns], (uint32_t)((i / ns) & 1), nullptr, 1u << 22);
     }
   } else {
     // ---- consumers: 16-token units, unit u of block u / upb taken by warp u % kConsumers ----
@@ -183,8 +192,8 @@ __global__ void __launch_bounds__(Cfg<NC>::kThreads, 1)
     }
     const uint32_t ring_s = sm100::smem_u32(ring);
     for (int u = warp; u < nb * upb && ok; u += kConsumers) {
-      const int i = u / upb, t = u - i * upb, st = i % kStages;
-      if (!sm100::mbar_wait(&full[st], (uint32_t)((i / kStages) & 1), a.status)) {
+      const int i = u / upb, t = u - i * upb, st = i % ns;
+      if (!sm100::mbar_wait(&full[st], (uint32_t)((i / ns) & 1), a.status)) {
         ok = false;
         break;
       }
@@ -390,7 +399,12 @@ void launch_hd_nc(const AttnDecodeArgs& a, int64_t cache_rows, cudaStream_t s, b
   t.status = a.status;
   const CUtensorMap tk = kv_map(a.k_cache, cache_rows, HD, a.block_size);
   const CUtensorMap tv = kv_map(a.v_cache, cache_rows, HD, a.block_size);
-  const size_t smem = 1024 + (size_t)kStages * 2 * a.block_size * HD * 2;
+  static const int env_stages = [] {
+    const char* e = getenv("HK_ATTN_STAGES");
+    return e && atoi(e) == 2 ? 2 : kStages;
+  }();
+  t.stages = a.block_size == 16 ? kStages : env_stages;
+  const size_t smem = 1024 + (size_t)t.stages * 2 * a.block_size * HD * 2;
   auto kern = attn_decode_tc_kernel<HD, NC>;
   HK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   launch_cluster(kern, dim3(a.num_splits, a.nkv, a.R), dim3(Cfg<NC>::kThreads), smem, s, pdl, a.num_splits, tk, tv, t);

@@ -41,6 +41,8 @@
 // Parity: crates/hawking-core/shaders/quant.metal gemm_q4_k_m_fused* (f32 activations, the
 // reference's default; its W4A8 GEMV is held off as quality-blocked in
 // workspace/docs/reference/env_flags.md:38); Q4_K formula crates/hawking-core/src/quant.rs:34-160.
+#include <cstdlib>
+
 #include "mma_gemv.cuh"
 #include "mg_device.cuh"
 #include "sm100.cuh"
@@ -51,8 +53,14 @@ namespace mg {
 
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
-constexpr int kStages = 2;           // ring stages per warp
-constexpr int kTpc = 2;              // tiles per stage (one bulk copy each)
+#ifndef HK_MG_STAGES
+#define HK_MG_STAGES 2
+#endif
+#ifndef HK_MG_TPC
+#define HK_MG_TPC 2
+#endif
+constexpr int kStages = HK_MG_STAGES;  // ring stages per warp
+constexpr int kTpc = HK_MG_TPC;        // tiles per stage (one bulk copy each)
 constexpr int kScaleBytes = 16 * 8 * 8;  // per warp: [16 rows][8 sub-blocks] float2 (S16, M'')
 constexpr int kMaxCtasPerSm = 3;         // resident CTAs per SM (the partial scratch is sized for this)
 
@@ -512,6 +520,19 @@ size_t smem_bytes(int fmt, int math, int xin, int nb, int K) {
   return s;
 }
 
+// CTAs per SM a launch may use (HK_MG_PER_SM, default: as many as fit, at most kMaxCtasPerSm).
+// Fewer leave shared memory free on every SM for the next kernel of the chain, whose CTAs then
+// become resident at the programmatic launch and stream their first weight tiles while this
+// kernel finishes.
+inline int per_sm_cap() {
+  static const int cap = [] {
+    const char* e = getenv("HK_MG_PER_SM");
+    const int v = e ? atoi(e) : 0;
+    return v >= 1 && v <= kMaxCtasPerSm ? v : kMaxCtasPerSm;
+  }();
+  return cap;
+}
+
 template <int FMT, int MATH, int XIN, int EPI>
 void dispatch_nb(const MgArgs& a, int sms, cudaStream_t st, bool pdl) {
   const size_t smem = smem_bytes(FMT, MATH, XIN, a.nb, a.K);
@@ -519,7 +540,8 @@ void dispatch_nb(const MgArgs& a, int sms, cudaStream_t st, bool pdl) {
     HK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     int per_sm = 1;
     HK_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem));
-    per_sm = per_sm < 1 ? 1 : (per_sm > kMaxCtasPerSm ? kMaxCtasPerSm : per_sm);
+    const int cap = per_sm_cap();
+    per_sm = per_sm < 1 ? 1 : (per_sm > cap ? cap : per_sm);
     launch(kern, dim3(sms * per_sm), dim3(kThreads), smem, st, pdl, a);
   };
   if (a.nb == 1) go(mg_gemv_kernel<FMT, MATH, 1, XIN, EPI>);

@@ -124,9 +124,10 @@ class Engine:
     @staticmethod
     def build_deepseek(cfg: ModelConfig, weights, device="cuda", max_batch: int = 8, max_ctx: Optional[int] = None,
                        block_size: int = 64, num_blocks: Optional[int] = None, kv_fraction: float = 0.5,
-                       policy: int = 0, tp=None):
-        """Engine around the MLA + MoE model (paged latent cache; forwards of <= 8 rows, several
-        rows of one sequence allowed: prompts prefill in 8-token chunks)."""
+                       policy: int = 0, tp=None, prefill_rows: int = 512):
+        """Engine around the MLA + MoE model (paged latent cache; decode forwards of <= 8 rows;
+        prompts prefill in forwards of up to ``prefill_rows`` rows on one GPU, 8 under tensor
+        parallelism)."""
         from ..models.deepseek import LAT, ROPE, DeepSeekModel, LatentCache
         max_ctx = max_ctx or cfg.max_ctx
         max_blocks = -(-max_ctx // block_size)
@@ -135,13 +136,13 @@ class Engine:
             bpb = cfg.layers * block_size * (LAT + ROPE) * 2
             num_blocks = min(int(free * kv_fraction // bpb), (max_batch + 1) * max_blocks + 16)
         kv = LatentCache(cfg.layers, num_blocks, block_size, max_batch + 1, max_blocks, device)
-        model = DeepSeekModel(cfg, weights, kv, max_rows=8, device=device, tp=tp)
-        return Engine(cfg, model, kv, max_batch=max_batch, max_prefill_tokens=8, policy=policy)
+        model = DeepSeekModel(cfg, weights, kv, max_rows=prefill_rows if tp is None else 8, device=device, tp=tp)
+        return Engine(cfg, model, kv, max_batch=max_batch, max_prefill_tokens=model.row_limit, policy=policy)
 
     @staticmethod
     def build_qwen_next(cfg: ModelConfig, weights, device="cuda", max_batch: int = 8, max_ctx: Optional[int] = None,
                         block_size: int = 64, num_blocks: Optional[int] = None, kv_fraction: float = 0.5,
-                        policy: int = 0, tp=None):
+                        policy: int = 0, tp=None, prefill_rows: int = 512):
         """Engine around the hybrid DeltaNet / gated-attention model: paged KV for the full-
         attention layers, one recurrent-state slot per block-table row (reset when a sequence
         starts), no prefix reuse (a cached prefix would not restore the recurrent state), and
@@ -157,8 +158,11 @@ class Engine:
             num_blocks = min(int(free * kv_fraction // bpb), (max_batch + 1) * max_blocks + 16)
         kv = PagedKVCache(max(1, n_full), cfg.n_kv_heads, cfg.head_dim, num_blocks, block_size, max_batch + 1,
                           max_blocks, device, prefix_cache=False)
-        model = QwenNextModel(cfg, weights, kv, max_rows=8, max_seqs=max_batch + 1, device=device, tp=tp)
-        return Engine(cfg, model, kv, max_batch=max_batch, max_prefill_tokens=8 * max_batch, policy=policy)
+        # prompts prefill in forwards of up to prefill_rows rows on one GPU (8 under tensor parallelism)
+        model = QwenNextModel(cfg, weights, kv, max_rows=prefill_rows if tp is None else 8, max_seqs=max_batch + 1,
+                              device=device, tp=tp)
+        return Engine(cfg, model, kv, max_batch=max_batch, max_prefill_tokens=max(model.row_limit, 8 * max_batch),
+                      policy=policy)
 
     @staticmethod
     def from_config(cfg: ModelConfig, weights, config, device="cuda", tp=None) -> "Engine":

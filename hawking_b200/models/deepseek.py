@@ -146,7 +146,12 @@ class DeepSeekModel:
         self.cfg, self.w, self.kv, self.dev = cfg, w, kv, torch.device(device)
         self.tp = tp
         self.mla_flash = True  # latent attention on the tensor cores (mla_flash.cu)
-        self.max_rows = R = min(max_rows, 8)
+        # decode takes up to 8 rows; on one GPU a prompt prefills in forwards of up to max_rows rows
+        # (the latent cache makes multi-row prefill exact; the absorb / output kernels run in
+        # 8-row slices, the experts' kernels read each expert's weights once per CTA for all of its
+        # pairs); tensor-parallel forwards stay at 8 rows (push all-reduce sites)
+        self.max_rows = R = max_rows if tp is None else min(max_rows, 8)
+        self.max_logit_rows = min(R, 64)  # rows whose logits one forward can return
         dev = self.dev
         H, nh = cfg.hidden, cfg.n_heads
         nope, rd, vd = cfg.qk_nope_dim, cfg.qk_rope_dim, cfg.v_head_dim
@@ -181,7 +186,8 @@ class DeepSeekModel:
         self.gx = Q8Act(R * k + R, H, dev)
         self.hx = Q8Act(R * k + R, F, dev)
         self.hs = Q8Act(R, Fs, dev)
-        self.logits = torch.zeros(R, cfg.vocab, device=dev)
+        self.logits = torch.zeros(self.max_logit_rows, cfg.vocab, device=dev)
+        self.xh = Q8Act(self.max_logit_rows, H, dev)  # normed rows of the requested logits
         self.next_ids = torch.zeros(R, dtype=torch.int32, device=dev)
         from .deepseek_gguf import yarn_attention_scale, yarn_freq_factors
         self.rope = ops.rope_table(cfg.max_ctx, ROPE, cfg.rope_theta, yarn_freq_factors(cfg), dev)
@@ -224,8 +230,10 @@ class DeepSeekModel:
         ops.launches.add(4)
         K.mla_kv_append(self.kva[:rows], L.kv_a_norm, cfg.eps, inp.positions[:rows], kv.block_tables,
                         inp.row_seq[:rows], self.rope, kv.latent[l], ops.PDL)
-        K.mla_absorb_q(self.q[:rows], L.w_uk, inp.positions[:rows], self.rope, self.q_lat[:rows], self.q_pe[:rows],
-                       ops.PDL)
+        for c0 in range(0, rows, 8):  # the absorb kernel takes up to 8 rows
+            c1 = min(rows, c0 + 8)
+            K.mla_absorb_q(self.q[c0:c1], L.w_uk, inp.positions[c0:c1], self.rope, self.q_lat[c0:c1],
+                           self.q_pe[c0:c1], ops.PDL)
         # num_splits 0: the tensor-core kernel (mla_flash.cu, picks its own splits) for 4+ rows, where it
         # measured 2.4x faster at 8 rows; fewer rows stay on the CUDA-core kernel (as fast at 64 heads,
         # faster for tensor-parallel head shards)
@@ -233,7 +241,9 @@ class DeepSeekModel:
         K.mla_decode(self.q_lat[:rows], self.q_pe[:rows], kv.latent[l], kv.block_tables, inp.row_seq[:rows],
                      inp.row_ctx[:rows], self.scale, 0 if flash else self.num_splits(rows),
                      self.o_lat[:rows], self.status, ops.PDL)
-        K.mla_out(self.o_lat[:rows], L.w_uv, self.attq.q[:rows], self.attq.d[:rows], self.attq.s[:rows], ops.PDL)
+        for c0 in range(0, rows, 8):
+            c1 = min(rows, c0 + 8)
+            K.mla_out(self.o_lat[c0:c1], L.w_uv, self.attq.q[c0:c1], self.attq.d[c0:c1], self.attq.s[c0:c1], ops.PDL)
         if self.tp is not None:
             mixed_gemv_push(t, L.idx["o"], self.attq.view(rows), self.tp, 2 * l)
         else:
@@ -260,7 +270,8 @@ class DeepSeekModel:
         if tp is not None and L.shared_here and not fold:
             raise NotImplementedError("expert parallel: the shared expert must have the routed experts' shape")
         K = kernels()
-        if self.fused_route:
+        fused = self.fused_route and rows <= 8
+        if fused:
             # one launch: router GEMV, top-k, sort by expert, active list (this rank's experts only
             # under expert parallelism); experts read token rows
             ops.moe_route(L.router, xa, k, self.scoring, L.router_bias, cfg.n_groups, cfg.topk_groups, cfg.norm_topk,
@@ -283,7 +294,7 @@ class DeepSeekModel:
         ep = dict(e_lo=e_lo, e_count=self.w.e_count)
         K.moe_mixed_gemv(0, t.descs, L.idx["eg"], L.idx["eu"], F, H, k, self.counts, self.offsets, self.sorted,
                          self.active, self.n_active, na, gin.q, gin.d, gin.s, self.hx.q, self.hx.d,
-                         self.hx.s, None, None, ops.PDL, rows * k, self.fused_route, **ep)
+                         self.hx.s, None, None, ops.PDL, rows * k, fused, **ep)
         if tp is not None:
             # expert-parallel combine: per-token sum over this rank's experts, pushed to every rank
             K.moe_mixed_gemv(2, t.descs, L.idx["ed"], L.idx["ed"], H, F, k, self.counts, self.offsets, self.sorted,
@@ -304,22 +315,35 @@ class DeepSeekModel:
         the first rows (all rows are computed; at most 8)."""
         if self.tp is not None:
             self._forward_tp(rows, sample, advance)
+            compact_logit_rows(self, n_logits)
         else:
-            self._forward_local(rows, sample, advance)
-        compact_logit_rows(self, n_logits)
+            self._forward_local(rows, sample, advance, n_logits)
 
-    def _forward_local(self, rows: int, sample: str = "greedy", advance: bool = False):
+    def _forward_local(self, rows: int, sample: str = "greedy", advance: bool = False, n_logits: int = 0):
         cfg, w, inp = self.cfg, self.w, self.inp
+        nl = n_logits or rows
+        if nl > self.max_logit_rows:
+            raise ValueError(f"forward: logits for {nl} rows requested, at most {self.max_logit_rows}")
         ops.embed(w.embed, inp.ids[:rows], self.x[:rows])
         for l, L in enumerate(w.layers):
             ops.rmsnorm_q8(self.x[:rows], L.attn_norm, cfg.eps, self.xa.view(rows))
             self._attention(l, L, rows)
             ops.rmsnorm_q8(self.x[:rows], L.ffn_norm, cfg.eps, self.xa.view(rows))
             self._ffn(L, rows)
+        if n_logits < 0:  # no row of this forward is sampled
+            if advance:
+                ops.advance(inp.ids, self.next_ids, inp.positions, inp.row_ctx, rows)
+            return
         ops.rmsnorm_q8(self.x[:rows], w.out_norm, cfg.eps, self.xa.view(rows))
-        mixed_gemv(w.table, w.lm_head, self.xa.view(rows), self.logits[:rows])
+        xh = self.xa.view(rows)
+        if n_logits:  # only the requested rows go through the LM head, in request order
+            idx = self.logit_rows[:nl].long()
+            for src, dst in ((self.xa.q, self.xh.q), (self.xa.d, self.xh.d), (self.xa.s, self.xh.s)):
+                torch.index_select(src, 0, idx, out=dst[:nl])
+            xh = self.xh.view(nl)
+        mixed_gemv(w.table, w.lm_head, xh, self.logits[:nl])
         if sample == "greedy":
-            ops.argmax(self.logits[:rows], self.next_ids[:rows])
+            ops.argmax(self.logits[:nl], self.next_ids[:nl])
         if advance:
             ops.advance(inp.ids, self.next_ids, inp.positions, inp.row_ctx, rows)
 
@@ -375,8 +399,9 @@ class DeepSeekModel:
         kv.sync_tables([seq_id])
         r = kv.row(seq_id)
         out = torch.empty(n, self.cfg.vocab, device=self.dev)
-        for c0 in range(0, n, self.max_rows):
-            c1 = min(n, c0 + self.max_rows)
+        step = min(self.max_rows, self.max_logit_rows)
+        for c0 in range(0, n, step):
+            c1 = min(n, c0 + step)
             pos = list(range(start_pos + c0, start_pos + c1))
             self.inp.upload(tokens[c0:c1], pos, [0] * (c1 - c0), [r] * (c1 - c0), [p + 1 for p in pos])
             self.forward(c1 - c0, "greedy")

@@ -167,7 +167,11 @@ class QwenNextModel:
         sites per layer (mixer output, expert combine), each consumed by the next RMSNorm."""
         self.cfg, self.w, self.kv, self.dev = cfg, w, kv, torch.device(device)
         self.tp = tp
-        self.max_rows = R = min(max_rows, 8)
+        # decode takes up to 8 rows; a prompt prefills in forwards of up to max_rows rows (every
+        # kernel loops its rows; the expert kernels read each expert's codes once per CTA for all
+        # of its pairs); tensor-parallel forwards stay at 8 rows (push all-reduce sites)
+        self.max_rows = R = max_rows if tp is None else min(max_rows, 8)
+        self.max_logit_rows = min(R, 64)  # rows whose logits one forward can return
         dev = self.dev
         H, nh, nkv, hd = cfg.hidden, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
         dm = self.dm = dims(cfg)
@@ -213,7 +217,8 @@ class QwenNextModel:
         self.hx = Q8Act(R * k + R, F, dev)
         self.hs = Q8Act(R, Fs, dev)
         # this rank's vocabulary slice under tensor parallelism
-        self.logits = torch.zeros(R, w.table.weights[w.lm_head].N, device=dev)
+        self.logits = torch.zeros(self.max_logit_rows, w.table.weights[w.lm_head].N, device=dev)
+        self.xh = Q8Act(self.max_logit_rows, H, dev)  # normed rows of the requested logits
         if tp is not None:
             if not self.fused_route:
                 raise ValueError("qwen3next tensor parallelism needs the fused routing kernel (hidden % 512 == 0)")
@@ -319,7 +324,8 @@ class QwenNextModel:
         xa = self.xa.view(rows)
         ops.router_logits(L.shared_gate, xa, self.sglog[:rows])
         K = kernels()
-        if self.fused_route:  # router GEMV, top-k, sort by expert and active list in one launch
+        fused = self.fused_route and rows <= 8
+        if fused:  # router GEMV, top-k, sort by expert and active list in one launch
             ops.moe_route(L.router, xa, k, 0, None, 1, 1, cfg.norm_topk, 1.0, self.rlog[:rows], self.ids[:rows],
                           self.rw[:rows], self.counts, self.offsets, self.sorted, self.active, self.n_active, False,
                           self.route_counter)
@@ -335,7 +341,7 @@ class QwenNextModel:
         na = min(E, rows * k)
         K.moe_mixed_gemv(0, t.descs, L.idx["eg"], L.idx["eu"], F, H, k, self.counts, self.offsets, self.sorted,
                          self.active, self.n_active, na, gin.q, gin.d, gin.s, self.hx.q, self.hx.d,
-                         self.hx.s, None, None, ops.PDL, rows * k, self.fused_route)
+                         self.hx.s, None, None, ops.PDL, rows * k, fused)
         K.moe_mixed_gemv(1, t.descs, L.idx["ed"], L.idx["ed"], H, F, k, self.counts, self.offsets, self.sorted,
                          self.active, self.n_active, na, self.hx.q, self.hx.d, self.hx.s, None, None, None,
                          self.x[:rows], self.rw[:rows].reshape(-1), ops.PDL)
@@ -348,10 +354,12 @@ class QwenNextModel:
         the first rows. Rows must belong to distinct sequences (``serial_rows``)."""
         from .deepseek import compact_logit_rows
         if self.tp is not None:
+            if rows > 8:
+                raise RuntimeError("tensor-parallel qwen3next forwards take at most 8 rows")
             self._forward_tp(rows, sample, advance)
+            compact_logit_rows(self, n_logits)
         else:
-            self._forward(rows, sample, advance)
-        compact_logit_rows(self, n_logits)
+            self._forward(rows, sample, advance, n_logits)
 
     def _forward_tp(self, rows: int, sample: str, advance: bool):
         cfg, w, inp, tp = self.cfg, self.w, self.inp, self.tp
@@ -392,8 +400,11 @@ class QwenNextModel:
             self._tp_full = torch.zeros(self.logits.shape[0], self.logits.shape[1] * self.tp.world, device=self.dev)
         return gather_vocab_logits(self.tp, self.logits[:nl], self._tp_full)
 
-    def _forward(self, rows: int, sample: str = "greedy", advance: bool = False):
+    def _forward(self, rows: int, sample: str = "greedy", advance: bool = False, n_logits: int = 0):
         cfg, w, inp = self.cfg, self.w, self.inp
+        nl = n_logits or rows
+        if nl > self.max_logit_rows:
+            raise ValueError(f"forward: logits for {nl} rows requested, at most {self.max_logit_rows}")
         ops.embed(w.embed, inp.ids[:rows], self.x[:rows])
         for l, L in enumerate(w.layers):
             ops.rmsnorm_q8(self.x[:rows], L.attn_norm, cfg.eps, self.xa.view(rows))
@@ -403,10 +414,20 @@ class QwenNextModel:
                 self._linear(l, L, rows)
             ops.rmsnorm_q8(self.x[:rows], L.post_norm, cfg.eps, self.xa.view(rows))
             self._moe(L, rows)
+        if n_logits < 0:  # no row of this forward is sampled
+            if advance:
+                ops.advance(inp.ids, self.next_ids, inp.positions, inp.row_ctx, rows)
+            return
         ops.rmsnorm_q8(self.x[:rows], w.out_norm, cfg.eps, self.xa.view(rows))
-        mixed_gemv(w.table, w.lm_head, self.xa.view(rows), self.logits[:rows])
+        xh = self.xa.view(rows)
+        if n_logits:  # only the requested rows go through the LM head, in request order
+            idx = self.logit_rows[:nl].long()
+            for src, dst in ((self.xa.q, self.xh.q), (self.xa.d, self.xh.d), (self.xa.s, self.xh.s)):
+                torch.index_select(src, 0, idx, out=dst[:nl])
+            xh = self.xh.view(nl)
+        mixed_gemv(w.table, w.lm_head, xh, self.logits[:nl])
         if sample == "greedy":
-            ops.argmax(self.logits[:rows], self.next_ids[:rows])
+            ops.argmax(self.logits[:nl], self.next_ids[:nl])
         if advance:
             ops.advance(inp.ids, self.next_ids, inp.positions, inp.row_ctx, rows)
 
@@ -422,8 +443,9 @@ class QwenNextModel:
         if start_pos == 0:
             self.reset_state(r)
         out = torch.empty(n, self.logits.shape[1], device=self.dev)  # this rank's vocabulary slice under TP
-        for c0 in range(0, n, self.max_rows):
-            c1 = min(n, c0 + self.max_rows)
+        step = min(self.max_rows, self.max_logit_rows)
+        for c0 in range(0, n, step):
+            c1 = min(n, c0 + step)
             p0 = start_pos + c0
             slots = kv.bm.slots(seq_id, p0, start_pos + c1)
             pos = list(range(p0, start_pos + c1))

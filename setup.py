@@ -55,6 +55,8 @@ if os.environ.get("HK_SKIP_CUDA", "0") != "1":
     ]
     if os.environ.get("HK_BOUNDS", "0") == "1":
         NVCC_FLAGS.append("-DHK_BOUNDS=1")
+    # tuning builds: extra preprocessor definitions, e.g. HK_NVCC_DEFINES="HK_MG_STAGES=4 HK_MG_TPC=1"
+    NVCC_FLAGS += ["-D" + d for d in os.environ.get("HK_NVCC_DEFINES", "").split()]
     ext_modules.append(
         CUDAExtension(
             "hawking_b200._kernels",
