@@ -125,6 +125,96 @@ void moe_active(const Tensor& counts, const Tensor& active, const Tensor& n_acti
   hk::moe_active_launch(ptr<int>(counts), (int)counts.numel(), ptr<int>(active), ptr<int>(n_active), cur_stream(), pdl);
 }
 
+using bf16_t = __nv_bfloat16;
+static const bf16_t* bfp(const Tensor& t) { return reinterpret_cast<const bf16_t*>(t.data_ptr()); }
+static bf16_t* bfpm(const Tensor& t) { return reinterpret_cast<bf16_t*>(t.data_ptr()); }
+
+void mixed_dequant_bf16(const Tensor& descs, const Tensor& didx, const Tensor& drow, int64_t rows, int64_t K,
+                        const Tensor& out, bool pdl) {
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.stride(-1) == 1, "mixed_dequant_bf16: bf16 rows");
+  TORCH_CHECK(didx.scalar_type() == at::kInt && drow.scalar_type() == at::kInt && didx.numel() == drow.numel(),
+              "mixed_dequant_bf16: int32 index / row lists of one length");
+  const c10::cuda::CUDAGuard g(out.device());
+  hk::mixed_dequant_bf16_launch(reinterpret_cast<const hk::MixedDesc*>(descs.data_ptr()), didx.data_ptr<int>(),
+                                drow.data_ptr<int>(), (int)didx.numel(), (int)rows, (int)K, bfpm(out), out.stride(0),
+                                cur_stream(), pdl);
+}
+
+void tc_gemm_bf16(const Tensor& w, const Tensor& x, int64_t N, int64_t M, const optional<Tensor>& y,
+                  const optional<Tensor>& h, bool atomic, bool y_zeroed, int64_t k_splits, int64_t bn,
+                  const Tensor& status, bool pdl, const optional<Tensor>& tiles, const optional<Tensor>& n_tiles,
+                  int64_t max_tiles, int64_t group_rows) {
+  TORCH_CHECK(w.scalar_type() == at::kBFloat16 && x.scalar_type() == at::kBFloat16 && w.stride(-1) == 1 &&
+              x.stride(-1) == 1 && w.size(1) == x.size(1), "tc_gemm_bf16: bf16 rows, same K");
+  hk::TcBf16Args g{};
+  g.w = bfp(w);
+  g.w_stride = w.stride(0);
+  g.w_rows = (int)w.size(0);
+  g.N = (int)N;
+  g.K = (int)w.size(1);
+  g.x = bfp(x);
+  g.x_stride = x.stride(0);
+  g.x_rows = (int)x.size(0);
+  g.M = (int)M;
+  if (y.has_value()) {
+    TORCH_CHECK(y->scalar_type() == at::kFloat && y->stride(-1) == 1, "tc_gemm_bf16: fp32 rows out");
+    g.y = y->data_ptr<float>();
+    g.y_stride = y->stride(0);
+  }
+  if (h.has_value()) {
+    TORCH_CHECK(h->scalar_type() == at::kBFloat16 && h->stride(-1) == 1, "tc_gemm_bf16: bf16 SwiGLU rows out");
+    g.h = bfpm(*h);
+    g.h_stride = h->stride(0);
+  }
+  TORCH_CHECK(g.y || g.h, "tc_gemm_bf16: an output");
+  g.atomic = atomic;
+  g.y_zeroed = y_zeroed;
+  g.k_splits = (int)k_splits;
+  g.bn = (int)bn;
+  g.status = status.data_ptr<int>();
+  g.pdl = pdl;
+  if (tiles.has_value()) {
+    TORCH_CHECK(n_tiles.has_value() && tiles->scalar_type() == at::kInt, "tc_gemm_bf16: int32 tile list + count");
+    g.tiles = tiles->data_ptr<int>();
+    g.n_tiles = n_tiles->data_ptr<int>();
+    g.max_tiles = (int)max_tiles;
+    g.group_rows = (int)group_rows;
+  }
+  const c10::cuda::CUDAGuard guard(x.device());
+  hk::tc_gemm_bf16_launch(g, cur_stream());
+}
+
+void moe_tiles(const Tensor& counts, const Tensor& offsets, int64_t E1, int64_t bn, const Tensor& tiles,
+               const Tensor& n_tiles, bool pdl) {
+  const c10::cuda::CUDAGuard g(counts.device());
+  hk::moe_tiles_launch(counts.data_ptr<int>(), offsets.data_ptr<int>(), (int)E1, (int)bn, tiles.data_ptr<int>(),
+                       n_tiles.data_ptr<int>(), cur_stream(), pdl);
+}
+
+void moe_gather_bf16(const Tensor& sorted, int64_t PS, int64_t P, int64_t k, const Tensor& x, const Tensor& xg,
+                     const Tensor& pos, bool pdl) {
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && xg.scalar_type() == at::kBFloat16, "moe_gather_bf16: bf16 rows");
+  const c10::cuda::CUDAGuard g(x.device());
+  hk::moe_gather_bf16_launch(sorted.data_ptr<int>(), (int)PS, (int)P, (int)k, bfp(x), x.stride(0), (int)x.size(1),
+                             bfpm(xg), xg.stride(0), pos.data_ptr<int>(), cur_stream(), pdl);
+}
+
+void moe_combine(const Tensor& y, const Tensor& pos, const Tensor& w, int64_t T, int64_t k, bool shared,
+                 const optional<Tensor>& shared_gate, const Tensor& x, bool pdl) {
+  TORCH_CHECK(y.scalar_type() == at::kFloat && x.scalar_type() == at::kFloat, "moe_combine: fp32 rows");
+  const c10::cuda::CUDAGuard g(x.device());
+  hk::moe_combine_launch(y.data_ptr<float>(), y.stride(0), pos.data_ptr<int>(), w.data_ptr<float>(), (int)T, (int)k,
+                         shared, shared_gate.has_value() ? shared_gate->data_ptr<float>() : nullptr,
+                         shared_gate.has_value() ? (shared_gate->dim() > 1 ? shared_gate->stride(0) : 1) : 0,
+                         x.data_ptr<float>(), x.stride(0), (int)x.size(1), cur_stream(), pdl);
+}
+
+void q8_to_bf16(const Tensor& q, const Tensor& d, const Tensor& out, bool pdl) {
+  const c10::cuda::CUDAGuard g(q.device());
+  hk::q8_to_bf16_launch(q.data_ptr<int8_t>(), d.data_ptr<float>(), q.stride(0), d.stride(0), (int)q.size(0),
+                        (int)q.size(1), bfpm(out), out.stride(0), cur_stream(), pdl);
+}
+
 void moe_mixed_gemv(int64_t epi, const Tensor& descs, int64_t base0, int64_t base1, int64_t N, int64_t K, int64_t k,
                     const Tensor& counts, const Tensor& offsets, const Tensor& sorted, const Tensor& active,
                     const Tensor& n_active, int64_t max_active, const Tensor& xq, const Tensor& xd, const Tensor& xs,
@@ -408,6 +498,20 @@ void register_model_kernels(py::module_& m) {
         py::arg("status"), py::arg("pdl") = false);
   m.def("mla_out", &mla_out, py::arg("o_lat"), py::arg("w_uv"), py::arg("oq"), py::arg("od"), py::arg("os"),
         py::arg("pdl") = false);
+  m.def("mixed_dequant_bf16", &mixed_dequant_bf16, py::arg("descs"), py::arg("didx"), py::arg("drow"),
+        py::arg("rows"), py::arg("K"), py::arg("out"), py::arg("pdl") = false);
+  m.def("tc_gemm_bf16", &tc_gemm_bf16, py::arg("w"), py::arg("x"), py::arg("N"), py::arg("M"),
+        py::arg("y") = py::none(), py::arg("h") = py::none(), py::arg("atomic") = false, py::arg("y_zeroed") = false,
+        py::arg("k_splits") = 1, py::arg("bn") = 128, py::arg("status"), py::arg("pdl") = false,
+        py::arg("tiles") = py::none(), py::arg("n_tiles") = py::none(), py::arg("max_tiles") = 0,
+        py::arg("group_rows") = 0);
+  m.def("moe_tiles", &moe_tiles, py::arg("counts"), py::arg("offsets"), py::arg("E1"), py::arg("bn"),
+        py::arg("tiles"), py::arg("n_tiles"), py::arg("pdl") = false);
+  m.def("moe_gather_bf16", &moe_gather_bf16, py::arg("sorted"), py::arg("PS"), py::arg("P"), py::arg("k"),
+        py::arg("x"), py::arg("xg"), py::arg("pos"), py::arg("pdl") = false);
+  m.def("moe_combine", &moe_combine, py::arg("y"), py::arg("pos"), py::arg("w"), py::arg("T"), py::arg("k"),
+        py::arg("shared"), py::arg("shared_gate"), py::arg("x"), py::arg("pdl") = false);
+  m.def("q8_to_bf16", &q8_to_bf16, py::arg("q"), py::arg("d"), py::arg("out"), py::arg("pdl") = false);
   m.def("mixed_descs", &mixed_descs, py::arg("codes"), py::arg("scales"), py::arg("kind"), py::arg("bits"),
         py::arg("group"), py::arg("zeros") = std::vector<int64_t>{});
   m.def("codebook_gemv", &codebook_gemv, py::arg("codebooks"), py::arg("codes"), py::arg("rows"), py::arg("nchunk"),

@@ -397,6 +397,34 @@ struct TcGemmArgs {
 int tc_gemm_splits(int N, int M, int K, int bn, int sms);
 void tc_gemm_launch(const TcGemmArgs& g, cudaStream_t s);
 
+// The same tcgen05 GEMM with bf16 weights loaded by TMA (a dequantised copy of any format):
+// Y[M, N] (+)= X[M, K] W[N, K]^T, or h = silu(g) u (bf16) from a [gate | up] W of N = 2F rows.
+// Grouped: CTA row y takes tile (group, first row, end row) = tiles[3 y ..] while y < *n_tiles
+// (built on the device), reading weight rows group * group_rows + the tile's local rows; output
+// columns are local (N = group_rows). One launch runs every expert of a MoE layer.
+struct TcBf16Args {
+  const __nv_bfloat16* w;       // [w_rows, w_stride] bf16
+  int64_t w_stride;
+  int w_rows;
+  int N, K;
+  const __nv_bfloat16* x;       // [x_rows, x_stride] bf16
+  int64_t x_stride;
+  int x_rows;
+  int M;                        // rows of X the (ungrouped) product covers
+  float* y;                     // [*, y_stride] fp32
+  int64_t y_stride;
+  int atomic, y_zeroed, k_splits, bn;
+  __nv_bfloat16* h;             // SwiGLU output [*, h_stride] or null
+  int64_t h_stride;
+  const int* tiles;             // grouped tile list (device) or null
+  const int* n_tiles;
+  int max_tiles;                // grid rows launched (>= the number of tiles)
+  int group_rows;
+  int* status;
+  bool pdl;
+};
+void tc_gemm_bf16_launch(const TcBf16Args& g, cudaStream_t s);
+
 // SwiGLU over a fused [gate | up] fp32 GEMM output: h = silu(g) * u -> bf16, then zero the input
 // (ready for the next split-K accumulation).
 void swiglu_bf16_launch(float* gu, int64_t gu_stride, int M, int F, __nv_bfloat16* h, int64_t h_stride,
@@ -527,6 +555,19 @@ struct MixedGemvArgs {
   int64_t argmax_offset;
 };
 void mixed_gemv_launch(int epi, const MixedGemvArgs& a, cudaStream_t s, bool pdl);
+
+// ---- prefill of the mixed-codec MoE models (moe_prefill.cu) ----
+void mixed_dequant_bf16_launch(const MixedDesc* desc, const int* didx, const int* drow, int count, int rows, int K,
+                               __nv_bfloat16* out, int64_t out_stride, cudaStream_t s, bool pdl);
+void moe_tiles_launch(const int* counts, const int* offsets, int E1, int bn, int* tiles, int* n_tiles,
+                      cudaStream_t s, bool pdl);
+void moe_gather_bf16_launch(const int* sorted, int PS, int P, int k, const __nv_bfloat16* x, int64_t x_stride, int K,
+                            __nv_bfloat16* xg, int64_t xg_stride, int* pos, cudaStream_t s, bool pdl);
+void moe_combine_launch(const float* y, int64_t y_stride, const int* pos, const float* w, int T, int k, bool shared,
+                        const float* shared_gate, int64_t gate_stride, float* x, int64_t x_stride, int H,
+                        cudaStream_t s, bool pdl);
+void q8_to_bf16_launch(const int8_t* q, const float* d, int64_t q_stride, int64_t d_stride, int rows, int K,
+                       __nv_bfloat16* out, int64_t out_stride, cudaStream_t s, bool pdl);
 // HGRAVR02 outlier residual added into y [nb, >= N] (row_ptr [N + 1], cols / signs [nnz]).
 void sparse_residual_launch(const int* row_ptr, const int* cols, const int8_t* signs, float scale, int N,
                             const int8_t* xq, const float* xd, int K, int nb, float* y, int64_t y_stride,

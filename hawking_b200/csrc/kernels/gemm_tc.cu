@@ -78,6 +78,12 @@ struct TcArgs {
   __nv_bfloat16* h;   // SwiGLU output
   int64_t h_stride;
   int F;              // SwiGLU: FFN width (up rows start at F)
+  // grouped (ABF only): CTA row blockIdx.y takes tile tiles[3 y .. 3 y + 2] = (group g, first
+  // row, end row) of the gathered activations while y < *n_tiles; its weight rows are those of
+  // group g (g * group_rows + the local row), its output columns the local rows
+  const int* tiles;
+  const int* n_tiles;
+  int group_rows;
 };
 
 __device__ __forceinline__ uint32_t bf2_bits(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t*>(&v); }
@@ -98,7 +104,10 @@ __device__ __forceinline__ uint2 dq4(uint32_t v, int hi, __nv_bfloat162 s2, __nv
   return r;
 }
 
-template <int BN, bool SW>
+// ABF: the weights are bf16 [rows, K] already (a dequantised copy): warp 0 loads them with TMA
+// straight into the A stages (tm_hdr is their map, tm_qs unused) and the dequantisers only run
+// the epilogue.
+template <int BN, bool SW, bool ABF>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_q4k_kernel(const __grid_constant__ CUtensorMap tm_hdr, const __grid_constant__ CUtensorMap tm_qs,
                        const __grid_constant__ CUtensorMap tm_x, TcArgs a) {
@@ -115,7 +124,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // SW: n0 is the tile's first gate row (64 per tile); otherwise its first weight row
-  const int n0 = SW ? blockIdx.x * (BM / 2) : blockIdx.x * BM, m0 = blockIdx.y * BN;
+  const int n0 = SW ? blockIdx.x * (BM / 2) : blockIdx.x * BM;
+  int m0 = blockIdx.y * BN, m_end = a.M, nw0 = n0;  // nw0: first weight row in the (stacked) matrix
+  if (ABF && a.tiles) {
+    pdl_wait();  // the tile list comes from the previous kernel
+    if ((int)blockIdx.y >= *a.n_tiles) return;  // the whole CTA, before any barrier or TMEM use
+    const int* tl = a.tiles + 3 * blockIdx.y;
+    nw0 = n0 + tl[0] * a.group_rows;
+    m0 = tl[1];
+    m_end = tl[2];
+  }
   const int s0 = blockIdx.z * a.stages_per_split;
   const int s1 = min(a.stages_total, s0 + a.stages_per_split);
   const int nst = max(0, s1 - s0);
@@ -123,7 +141,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < L::DR; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], kDequantWarps); }
-    for (int i = 0; i < DA; ++i) { mbar_init(&a_full[i], kDequantWarps + 1); mbar_init(&a_empty[i], 1); }
+    for (int i = 0; i < DA; ++i) { mbar_init(&a_full[i], ABF ? 2 : kDequantWarps + 1); mbar_init(&a_empty[i], 1); }
     mbar_init(acc_full, 1);
     fence_barrier_init();
   }
@@ -133,11 +151,33 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // Weights do not depend on the previous kernel: only the raw producer skips the PDL wait.
-  if (!(warp == 0)) pdl_wait();
+  // Weights do not depend on the previous kernel: only the raw producer skips the PDL wait
+  // (a dequantised bf16 copy does: every warp waits).
+  if (ABF || warp != 0) pdl_wait();
 
   if (nst > 0) {
-    if (warp == 0 && lane == 0) {
+    if (ABF && warp == 0 && lane == 0) {
+      // ---- bf16 weight producer: TMA straight into the A stages ----
+      int issued = 0;
+      for (int i = 0; i < nst; ++i) {
+        const int slot = i % DA;
+        if (!mbar_wait(&a_empty[slot], ((i / DA) & 1) ^ 1, a.status)) break;
+        const int gs = s0 + i;
+        mbar_arrive_expect_tx(&a_full[slot], A_STAGE);
+        uint8_t* as = smem + L::off_a + slot * A_STAGE;
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          if constexpr (SW) {  // 64 gate rows, then the 64 matching up rows
+            tma_load_2d(as + c * A_ATOM, &tm_hdr, gs * BK + c * 64, nw0, &a_full[slot]);
+            tma_load_2d(as + c * A_ATOM + A_ATOM / 2, &tm_hdr, gs * BK + c * 64, a.F + nw0, &a_full[slot]);
+          } else {
+            tma_load_2d(as + c * A_ATOM, &tm_hdr, gs * BK + c * 64, nw0, &a_full[slot]);
+          }
+        }
+        ++issued;
+      }
+      for (int i = max(0, issued - DA); i < issued; ++i) mbar_wait(&a_full[i % DA], (i / DA) & 1, nullptr, 1u << 22);
+    } else if (!ABF && warp == 0 && lane == 0) {
       // ---- raw Q4_K producer ----
       int issued = 0;
       for (int i = 0; i < nst; ++i) {
@@ -198,7 +238,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (a.serialize) ok = mbar_wait(&a_empty[slot], (i / DA) & 1, a.status);  // debug: no MMA/dequant overlap
       }
       umma_commit(acc_full);
-    } else if (warp >= kDequantWarp0 && warp < kDequantWarp0 + kDequantWarps) {
+    } else if (!ABF && warp >= kDequantWarp0 && warp < kDequantWarp0 + kDequantWarps) {
       // ---- dequantisers ----
       const int t = (warp - kDequantWarp0) * 32 + lane;
       const int r = t >> 1, c = t & 1;
@@ -272,7 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             const int m = m0 + j * 8 + e;
-            if (m < a.M) a.h[(int64_t)m * a.h_stride + f] = __float2bfloat16(v[e] / (1.f + __expf(-v[e])) * u[e]);
+            if (m < m_end) a.h[(int64_t)m * a.h_stride + f] = __float2bfloat16(v[e] / (1.f + __expf(-v[e])) * u[e]);
           }
         }
       }
@@ -290,7 +330,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             const int m = m0 + j * 8 + e;
-            if (m < a.M && n < a.N) {
+            if (m < m_end && n < a.N) {
               float* dst = a.y + (int64_t)m * a.y_stride + n;
               if (a.atomic) atomicAdd(dst, v[e]);
               else *dst = v[e];
@@ -863,11 +903,11 @@ void launch_bn(const TcGemmArgs& g, cudaStream_t s) {
   if (SW && splits != 1) throw std::runtime_error("tc_gemm swiglu: no split-K");
   static bool attr_set = false;
   if (!attr_set) {
-    HK_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_q4k_kernel<BN, SW>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::total));
+    HK_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_q4k_kernel<BN, SW, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::total));
     attr_set = true;
   }
   dim3 grid(g.N / BM, (g.M + BN - 1) / BN, splits);
-  launch(tc_gemm_q4k_kernel<BN, SW>, grid, dim3(kThreads), L::total, s, g.pdl, tm_hdr, tm_qs, tm_x, a);
+  launch(tc_gemm_q4k_kernel<BN, SW, false>, grid, dim3(kThreads), L::total, s, g.pdl, tm_hdr, tm_qs, tm_x, a);
 }
 
 template <int BN, bool SW>
@@ -964,7 +1004,72 @@ void launch_pair(const TcGemmArgs& g, cudaStream_t s) {
                  tm_x, a);
 }
 
+template <int BN, bool SW>
+void launch_abf(const TcBf16Args& g, cudaStream_t s) {
+  using L = Layout<BN>;
+  const uint32_t box_rows = SW ? BM / 2 : BM;
+  CUtensorMap tm_a = make_map_2d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, g.w, g.K, g.w_rows, (uint64_t)g.w_stride * 2, 64,
+                                 box_rows, CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tm_x = make_map_2d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, g.x, g.K, g.x_rows, (uint64_t)g.x_stride * 2, 64, BN,
+                                 CU_TENSOR_MAP_SWIZZLE_128B);
+  TcArgs a{};
+  a.N = g.N;
+  a.K = g.K;
+  a.M = g.M;
+  a.stages_total = g.K / BK;
+  int splits = g.tiles ? 1 : std::max(1, std::min(g.k_splits, a.stages_total));
+  a.stages_per_split = (a.stages_total + splits - 1) / splits;
+  splits = (a.stages_total + a.stages_per_split - 1) / a.stages_per_split;
+  a.y = g.y;
+  a.y_stride = g.y_stride;
+  a.atomic = (g.atomic || splits > 1) ? 1 : 0;
+  a.status = g.status;
+  a.h = g.h;
+  a.h_stride = g.h_stride;
+  a.F = SW ? g.N / 2 : 0;
+  a.tiles = g.tiles;
+  a.n_tiles = g.n_tiles;
+  a.group_rows = g.group_rows;
+  if (SW && splits != 1) throw std::runtime_error("tc_gemm bf16 swiglu: no split-K");
+  static bool attr_set = false;
+  if (!attr_set) {
+    HK_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_q4k_kernel<BN, SW, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       L::total));
+    attr_set = true;
+  }
+  const int ty = g.tiles ? g.max_tiles : (g.M + BN - 1) / BN;
+  if (ty <= 0) return;
+  dim3 grid((g.N + BM - 1) / BM, ty, splits);
+  launch(tc_gemm_q4k_kernel<BN, SW, true>, grid, dim3(kThreads), L::total, s, g.pdl, tm_a, tm_a, tm_x, a);
+}
+
 }  // namespace
+
+void tc_gemm_bf16_launch(const TcBf16Args& g, cudaStream_t s) {
+  // plain products may end in a partial 128-row weight tile (the TMA box reads zeros past the last
+  // row, the epilogue stores rows < N only); SwiGLU pairs and expert groups are whole tiles
+  if ((g.h || g.tiles) && g.N % BM) throw std::runtime_error("tc_gemm bf16: output rows must be a multiple of 128");
+  if (g.K % BK) throw std::runtime_error("tc_gemm bf16: K must be a multiple of 128");
+  if ((reinterpret_cast<uintptr_t>(g.w) | reinterpret_cast<uintptr_t>(g.x)) & 15 || (g.w_stride * 2) % 16 ||
+      (g.x_stride * 2) % 16)
+    throw std::runtime_error("tc_gemm bf16: operands must be 16-byte aligned rows");
+  if (g.tiles && (g.group_rows % BM || g.group_rows != g.N)) throw std::runtime_error("tc_gemm bf16 grouped: group rows");
+  if (g.k_splits > 1 && !g.atomic && !g.y_zeroed && !g.h) throw std::runtime_error("tc_gemm bf16: split-K needs a zeroed output");
+  if (g.h) {
+    switch (g.bn) {
+      case 64: launch_abf<64, true>(g, s); break;
+      case 128: launch_abf<128, true>(g, s); break;
+      default: throw std::runtime_error("tc_gemm bf16 swiglu: bn must be 64 or 128");
+    }
+    return;
+  }
+  switch (g.bn) {
+    case 32: launch_abf<32, false>(g, s); break;
+    case 64: launch_abf<64, false>(g, s); break;
+    case 128: launch_abf<128, false>(g, s); break;
+    default: throw std::runtime_error("tc_gemm bf16: bn must be 32, 64 or 128");
+  }
+}
 
 int tc_gemm_splits(int N, int M, int K, int bn, int sms) {
   const int tiles = (N / BM) * ((M + bn - 1) / bn);

@@ -124,7 +124,7 @@ class Engine:
     @staticmethod
     def build_deepseek(cfg: ModelConfig, weights, device="cuda", max_batch: int = 8, max_ctx: Optional[int] = None,
                        block_size: int = 64, num_blocks: Optional[int] = None, kv_fraction: float = 0.5,
-                       policy: int = 0, tp=None, prefill_rows: int = 512):
+                       policy: int = 0, tp=None, prefill_rows: int = 2048):
         """Engine around the MLA + MoE model (paged latent cache; decode forwards of <= 8 rows;
         prompts prefill in forwards of up to ``prefill_rows`` rows on one GPU, 8 under tensor
         parallelism)."""
@@ -142,7 +142,7 @@ class Engine:
     @staticmethod
     def build_qwen_next(cfg: ModelConfig, weights, device="cuda", max_batch: int = 8, max_ctx: Optional[int] = None,
                         block_size: int = 64, num_blocks: Optional[int] = None, kv_fraction: float = 0.5,
-                        policy: int = 0, tp=None, prefill_rows: int = 512):
+                        policy: int = 0, tp=None, prefill_rows: int = 2048):
         """Engine around the hybrid DeltaNet / gated-attention model: paged KV for the full-
         attention layers, one recurrent-state slot per block-table row (reset when a sequence
         starts), no prefix reuse (a cached prefix would not restore the recurrent state), and

@@ -194,6 +194,15 @@ class DeepSeekModel:
         self.scale = yarn_attention_scale(cfg)
         self.scoring = 1 if cfg.router == "sigmoid_bias" else 0  # router: sigmoid + bias, or softmax
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.prefill = None  # ops/prefill.py MoePrefill, made at the first forward of more than 8 rows
+        self.wide = None     # ops/prefill.py WideLinear (dense projections of wide forwards)
+        self.xb = self.qab = self.attb = self.hb = None
+        if tp is None and R > 8:  # bf16 rows of the wide forwards' tensor-core GEMMs
+            bf = dict(dtype=torch.bfloat16, device=dev)
+            self.xb = torch.zeros(R, H, **bf)
+            self.qab = torch.zeros(R, max(cfg.q_lora_rank, 32), **bf)
+            self.attb = torch.zeros(R, nh * vd, **bf)
+            self.hb = torch.zeros(R, max(cfg.ffn, 32), **bf)
         if tp is not None:
             self.x2 = torch.zeros(R, H, device=dev)  # second residual buffer of the push all-reduce
             self.argmax_slots = torch.zeros(R, ops.ARGMAX_SLOTS, dtype=torch.int64, device=dev)
@@ -212,11 +221,39 @@ class DeepSeekModel:
             s *= 2
         return s
 
+    def _wide(self, rows) -> bool:
+        """This forward's projections run as tensor-core GEMMs over bf16 rows (prefill)."""
+        if self.tp is not None or rows <= 8 or self.xb is None:
+            return False
+        c = self.cfg
+        if any(d % 128 for d in (c.hidden, c.q_lora_rank, c.n_heads * c.v_head_dim)):
+            return False  # the GEMM's K runs in 128-element stages
+        if self.wide is None:
+            from ..ops.prefill import WideLinear
+            self.wide = WideLinear(self.w.table, self.dev, self.status)
+        return True
+
     def _attention(self, l, L, rows):
         cfg, t, kv, inp = self.cfg, self.w.table, self.kv, self.inp
         K = kernels()
         xa = self.xa.view(rows)
-        if "q" in L.idx:  # no query low-rank: q and kv_a straight from the normed hidden
+        wide = self._wide(rows)
+        if wide:
+            W = self.wide
+            ops.rmsnorm(self.x[:rows], L.attn_norm, cfg.eps, yb=self.xb[:rows])
+            xb = self.xb[:rows]
+            if "q" in L.idx:
+                W.linear(L.idx["q"], xb, self.q[:rows])
+                W.linear(L.idx["kva"], xb, self.kva[:rows])
+            else:
+                if "qakva" in L.idx:
+                    W.linear(L.idx["qakva"], xb, self.qakva[:rows])
+                else:
+                    W.linear(L.idx["qa"], xb, self.qa[:rows])
+                    W.linear(L.idx["kva"], xb, self.kva[:rows])
+                ops.rmsnorm(self.qa[:rows], L.q_a_norm, cfg.eps, yb=self.qab[:rows, :cfg.q_lora_rank])
+                W.linear(L.idx["qb"], self.qab[:rows, :cfg.q_lora_rank], self.q[:rows])
+        elif "q" in L.idx:  # no query low-rank: q and kv_a straight from the normed hidden
             mixed_gemv(t, L.idx["q"], xa, self.q[:rows])
             mixed_gemv(t, L.idx["kva"], xa, self.kva[:rows])
         else:
@@ -246,6 +283,10 @@ class DeepSeekModel:
             K.mla_out(self.o_lat[c0:c1], L.w_uv, self.attq.q[c0:c1], self.attq.d[c0:c1], self.attq.s[c0:c1], ops.PDL)
         if self.tp is not None:
             mixed_gemv_push(t, L.idx["o"], self.attq.view(rows), self.tp, 2 * l)
+        elif wide:
+            from ..ops.prefill import q8_to_bf16
+            q8_to_bf16(self.attq.view(rows), self.attb[:rows])
+            self.wide.linear(L.idx["o"], self.attb[:rows], self.x[:rows], residual=True)
         else:
             mixed_gemv(t, L.idx["o"], self.attq.view(rows), self.x[:rows], residual=True)
 
@@ -254,6 +295,11 @@ class DeepSeekModel:
         every rank's receive region of ``site`` instead of added to the residual."""
         cfg, t, tp = self.cfg, self.w.table, self.tp
         xa = self.xa.view(rows)
+        if L.dense and self._wide(rows) and cfg.ffn % 64 == 0:
+            ops.rmsnorm(self.x[:rows], L.ffn_norm, cfg.eps, yb=self.xb[:rows])
+            self.wide.swiglu(L.idx["g"], L.idx["u"], self.xb[:rows], self.hb[:rows, :cfg.ffn])
+            self.wide.linear(L.idx["d"], self.hb[:rows, :cfg.ffn], self.x[:rows], residual=True)
+            return
         if L.dense:
             h = self.h.view(rows)
             mixed_gemv_swiglu(t, L.idx["g"], L.idx["u"], xa, h)
@@ -265,6 +311,9 @@ class DeepSeekModel:
         E, k, H, F = cfg.n_experts, cfg.top_k, cfg.hidden, cfg.expert_ffn
         ne = self.w.e_count or E  # routed experts in this rank's table
         e_lo = self.w.e_lo
+        if tp is None and rows > 8 and F % 128 == 0 and H % 128 == 0:
+            self._ffn_wide(L, rows)
+            return
         fold = self.fold_shared and L.shared_here and L.idx.get("sg") == L.idx["eg"] + ne and \
             L.idx.get("su") == L.idx["eu"] + ne and L.idx.get("sd") == L.idx["ed"] + ne
         if tp is not None and L.shared_here and not fold:
@@ -309,6 +358,27 @@ class DeepSeekModel:
             hs = self.hs.view(rows)
             mixed_gemv_swiglu(t, L.idx["sg"], L.idx["su"], xa, hs)
             mixed_gemv(t, L.idx["sd"], hs, self.x[:rows], residual=True)
+
+    def _ffn_wide(self, L, rows):
+        """Routed experts of a prefill forward on the tensor cores (ops/prefill.py): routing over
+        the q8 rows, experts as two grouped GEMMs over the bf16 normed rows, deterministic
+        combine; the shared expert folded in as one more group when it has the experts' width."""
+        from ..ops.prefill import MoePrefill
+        cfg, xa = self.cfg, self.xa.view(rows)
+        E, k = cfg.n_experts, cfg.top_k
+        if self.prefill is None:
+            self.prefill = MoePrefill(self.w.table, self.dev, E, cfg.expert_ffn, cfg.hidden,
+                                      self.max_rows * (k + 1), self.status)
+        ops.rmsnorm(self.x[:rows], L.ffn_norm, cfg.eps, yb=self.xb[:rows])
+        fold = "sg" in L.idx and cfg.shared_ffn == cfg.expert_ffn
+        ops.router_logits(L.router, xa, self.rlog[:rows])
+        ops.moe_topk(self.rlog[:rows], L.router_bias, k, self.scoring, cfg.n_groups, cfg.topk_groups, cfg.norm_topk,
+                     cfg.routed_scale, self.ids[:rows], self.rw[:rows])
+        ops.moe_align(self.ids[:rows], E, xa, self.counts, self.offsets, self.sorted, self.gx, shared=fold)
+        self.prefill.run(L.idx, rows, k, self.xb[:rows], self.x[:rows], self.counts, self.offsets, self.sorted,
+                         self.rw[:rows], fold, pdl=ops.PDL)
+        if not fold and "sg" in L.idx:
+            self.prefill.dense_shared(L.idx, cfg.shared_ffn, rows, self.xb, self.x, pdl=ops.PDL)
 
     def forward(self, rows: int, sample: str = "greedy", advance: bool = False, n_logits: int = 0):
         """``n_logits`` (engine): > 0 moves the logits / greedy ids of ``logit_rows[:n_logits]`` to

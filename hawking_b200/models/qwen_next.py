@@ -33,6 +33,9 @@ from ..ops.mixed import (BINARY, UNIFORM, MixedTable, MixedWeight, mixed_gemv, m
                          mixed_gemv_swiglu)
 from .config import ModelConfig
 
+# prefill forwards (> 8 rows) run the experts as grouped tensor-core GEMMs (0: the GEMV kernels)
+MOE_PREFILL = __import__("os").environ.get("HK_MOE_PREFILL", "1") == "1"
+
 
 @dataclass
 class QNLayer:
@@ -213,10 +216,19 @@ class QwenNextModel:
         self.n_active = torch.zeros(1, dtype=torch.int32, device=dev)
         self.route_counter = torch.zeros(1, dtype=torch.int32, device=dev)
         self.fused_route = cfg.hidden % 512 == 0 and E < 1024
-        self.gx = Q8Act(R * k, H, dev)
+        self.gx = Q8Act(R * k + R, H, dev)
         self.hx = Q8Act(R * k + R, F, dev)
         self.hs = Q8Act(R, Fs, dev)
         # this rank's vocabulary slice under tensor parallelism
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.prefill = None  # ops/prefill.py MoePrefill, made at the first forward of more than 8 rows
+        self.wide = None     # ops/prefill.py WideLinear (dense projections of wide forwards)
+        self.xb = self.attb = self.doutb = None
+        if tp is None and R > 8:  # bf16 rows of the wide forwards' tensor-core GEMMs
+            bf = dict(dtype=torch.bfloat16, device=dev)
+            self.xb = torch.zeros(R, H, **bf)
+            self.attb = torch.zeros(R, nh * hd, **bf)
+            self.doutb = torch.zeros(R, dm["vdim"], **bf)
         self.logits = torch.zeros(self.max_logit_rows, w.table.weights[w.lm_head].N, device=dev)
         self.xh = Q8Act(self.max_logit_rows, H, dev)  # normed rows of the requested logits
         if tp is not None:
@@ -250,15 +262,36 @@ class QwenNextModel:
             s *= 2
         return s
 
+    def _wide(self, rows) -> bool:
+        """This forward's projections run as tensor-core GEMMs over bf16 rows (prefill)."""
+        if self.tp is not None or rows <= 8 or self.xb is None:
+            return False
+        c, dm = self.cfg, self.dm
+        if any(d % 128 for d in (c.hidden, c.n_heads * c.head_dim, dm["vdim"])):
+            return False  # the GEMM's K runs in 128-element stages
+        if self.wide is None:
+            from ..ops.prefill import WideLinear
+            self.wide = WideLinear(self.w.table, self.dev, self.status)
+        return True
+
     def _full(self, l, L, rows, site: int = -1):
         cfg, w, kv, inp = self.cfg, self.w, self.kv, self.inp
         nh, nkv, hd = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
         t, xa = w.table, self.xa.view(rows)
         Qn, Kn = nh * hd, nkv * hd
-        mixed_gemv(t, L.idx["q"], xa, self.qkv[:rows, :Qn])
-        mixed_gemv(t, L.idx["k"], xa, self.qkv[:rows, Qn:Qn + Kn])
-        mixed_gemv(t, L.idx["v"], xa, self.qkv[:rows, Qn + Kn:])
-        mixed_gemv(t, L.idx["g"], xa, self.gate[:rows])
+        wide = site < 0 and self._wide(rows)
+        if wide:
+            ops.rmsnorm(self.x[:rows], L.attn_norm, cfg.eps, yb=self.xb[:rows])
+            xb, W = self.xb[:rows], self.wide
+            W.linear(L.idx["q"], xb, self.qkv[:rows, :Qn])
+            W.linear(L.idx["k"], xb, self.qkv[:rows, Qn:Qn + Kn])
+            W.linear(L.idx["v"], xb, self.qkv[:rows, Qn + Kn:])
+            W.linear(L.idx["g"], xb, self.gate[:rows])
+        else:
+            mixed_gemv(t, L.idx["q"], xa, self.qkv[:rows, :Qn])
+            mixed_gemv(t, L.idx["k"], xa, self.qkv[:rows, Qn:Qn + Kn])
+            mixed_gemv(t, L.idx["v"], xa, self.qkv[:rows, Qn + Kn:])
+            mixed_gemv(t, L.idx["g"], xa, self.gate[:rows])
         kl = self.full_index[l]
         ops.rope_append(self.qkv[:rows], inp.positions[:rows], None, self.rope, cfg.rope_dim, cfg.rope_style,
                         self.q[:rows], kv.k[kl], kv.v[kl], nh, nkv, hd, kv.block_size, q_norm=L.q_norm,
@@ -271,6 +304,10 @@ class QwenNextModel:
                                   self.attq.s[:rows], ops.PDL)
         if site >= 0:
             mixed_gemv_push(t, L.idx["o"], self.attq.view(rows), self.tp, site)
+        elif wide:
+            from ..ops.prefill import q8_to_bf16
+            q8_to_bf16(self.attq.view(rows), self.attb[:rows])
+            self.wide.linear(L.idx["o"], self.attb[:rows], self.x[:rows], residual=True)
         else:
             mixed_gemv(t, L.idx["o"], self.attq.view(rows), self.x[:rows], residual=True)
 
@@ -278,8 +315,14 @@ class QwenNextModel:
         cfg, t, dm, inp = self.cfg, self.w.table, self.dm, self.inp
         xa = self.xa.view(rows)
         li = self.lin_index[l]
-        mixed_gemv(t, L.idx["qkvz"], xa, self.qkvz[:rows])
-        mixed_gemv(t, L.idx["ba"], xa, self.ba[:rows])
+        wide = site < 0 and self._wide(rows)
+        if wide:
+            ops.rmsnorm(self.x[:rows], L.attn_norm, cfg.eps, yb=self.xb[:rows])
+            self.wide.linear(L.idx["qkvz"], self.xb[:rows], self.qkvz[:rows])
+            self.wide.linear(L.idx["ba"], self.xb[:rows], self.ba[:rows])
+        else:
+            mixed_gemv(t, L.idx["qkvz"], xa, self.qkvz[:rows])
+            mixed_gemv(t, L.idx["ba"], xa, self.ba[:rows])
         ops.launches.add(2)
         kernels().deltanet_conv(self.qkvz[:rows], L.conv_w, self.conv_state[li], inp.row_seq[:rows], dm["kh"], dm["r"],
                                 dm["dk"], dm["dv"], cfg.conv_kernel, cfg.eps, self.dq[:rows], self.dk_[:rows],
@@ -290,6 +333,10 @@ class QwenNextModel:
                                      self.dout.d[:rows], self.dout.s[:rows], ops.PDL)
         if site >= 0:
             mixed_gemv_push(t, L.idx["out"], self.dout.view(rows), self.tp, site)
+        elif wide:
+            from ..ops.prefill import q8_to_bf16
+            q8_to_bf16(self.dout.view(rows), self.doutb[:rows])
+            self.wide.linear(L.idx["out"], self.doutb[:rows], self.x[:rows], residual=True)
         else:
             mixed_gemv(t, L.idx["out"], self.dout.view(rows), self.x[:rows], residual=True)
 
@@ -324,6 +371,19 @@ class QwenNextModel:
         xa = self.xa.view(rows)
         ops.router_logits(L.shared_gate, xa, self.sglog[:rows])
         K = kernels()
+        if rows > 8 and cfg.shared_ffn == F and F % 128 == 0 and H % 128 == 0 and MOE_PREFILL:
+            # prefill: experts as two grouped tensor-core GEMMs (ops/prefill.py), the gated shared
+            # expert folded in as one more group weighted by sigmoid(its gate logit)
+            from ..ops.prefill import MoePrefill
+            if self.prefill is None:
+                self.prefill = MoePrefill(t, self.dev, E, F, H, self.max_rows * (k + 1), self.status)
+            ops.rmsnorm(self.x[:rows], L.post_norm, cfg.eps, yb=self.xb[:rows])
+            ops.router_logits(L.router, xa, self.rlog[:rows])
+            ops.moe_topk(self.rlog[:rows], None, k, 0, 1, 1, cfg.norm_topk, 1.0, self.ids[:rows], self.rw[:rows])
+            ops.moe_align(self.ids[:rows], E, xa, self.counts, self.offsets, self.sorted, self.gx, shared=True)
+            self.prefill.run(L.idx, rows, k, self.xb[:rows], self.x[:rows], self.counts, self.offsets, self.sorted,
+                             self.rw[:rows], True, shared_gate=self.sglog[:rows], pdl=ops.PDL)
+            return
         fused = self.fused_route and rows <= 8
         if fused:  # router GEMV, top-k, sort by expert and active list in one launch
             ops.moe_route(L.router, xa, k, 0, None, 1, 1, cfg.norm_topk, 1.0, self.rlog[:rows], self.ids[:rows],

@@ -32,7 +32,9 @@ def test_engine_deepseek_greedy_matches_model():
     eng = Engine.build_deepseek(cfg, w, device=DEV, max_batch=2, max_ctx=256, block_size=16, num_blocks=64)
     prompt = [5, 77, 300, 12, 9, 401, 256, 3, 44, 100]
     got = eng.generate([prompt], SamplingParams(max_tokens=5))[0]
-    ref_m = DeepSeekModel(cfg, w, LatentCache(cfg.layers, 64, 16, 2, 16, DEV), max_rows=8, device=DEV)
+    # the reference runs the prompt in forwards as wide as the engine's (same kernels, same rounding)
+    ref_m = DeepSeekModel(cfg, w, LatentCache(cfg.layers, 64, 16, 2, 16, DEV), max_rows=eng.model.row_limit,
+                          device=DEV)
     assert got == _greedy_reference(ref_m, prompt, 5)
     two = eng.generate([prompt, prompt[:4]], SamplingParams(max_tokens=3))
     assert [len(t) for t in two] == [3, 3]
@@ -51,7 +53,7 @@ def test_engine_qwen_next_waves_match_model():
     got = eng.generate([prompt], SamplingParams(max_tokens=5))[0]
     n_full = sum(cfg.layer_is_full_attention(l) for l in range(cfg.layers))
     kv = PagedKVCache(n_full, cfg.n_kv_heads, cfg.head_dim, 64, 16, 2, 16, DEV, prefix_cache=False)
-    ref_m = QwenNextModel(cfg, w, kv, max_rows=8, max_seqs=2, device=DEV)
+    ref_m = QwenNextModel(cfg, w, kv, max_rows=eng.model.row_limit, max_seqs=2, device=DEV)
     assert got == _greedy_reference(ref_m, prompt, 5, seq_id=1)
     # two sequences of different lengths advance in waves (one row per sequence per forward)
     two = eng.generate([prompt, prompt[:3]], SamplingParams(max_tokens=4))
