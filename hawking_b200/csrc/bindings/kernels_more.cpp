@@ -171,9 +171,10 @@ void moe_align(const Tensor& ids, int64_t E, const Tensor& xq, const Tensor& xd,
   a.counts = counts.data_ptr<int>();
   a.offsets = offsets.data_ptr<int>();
   a.sorted = sorted.data_ptr<int>();
-  a.gq = gq.data_ptr<int8_t>();
-  a.gd = gd.data_ptr<float>();
-  a.gs = gs.data_ptr<float>();
+  // empty gathered tensors: the counting sort only (the caller gathers its own rows)
+  a.gq = gq.numel() ? gq.data_ptr<int8_t>() : nullptr;
+  a.gd = gq.numel() ? gd.data_ptr<float>() : nullptr;
+  a.gs = gq.numel() ? gs.data_ptr<float>() : nullptr;
   const c10::cuda::CUDAGuard g(ids.device());
   hk::moe_align_launch(a, cur_stream(), pdl);
 }

@@ -324,8 +324,12 @@ __global__ void __launch_bounds__(1024) moe_align_kernel(MoeAlignArgs a) {
   }
   for (int t = tid; t < PS - P; t += blockDim.x) a.sorted[P + t] = P + t;  // shared bucket is last
   __syncthreads();
-  // Gather q8 activations in sorted order.
+  // Gather q8 activations in sorted order (unless the caller gathers its own rows).
   const int K = a.K;
+  if (!a.gq) {
+    pdl_launch();
+    return;
+  }
   for (int idx = tid; idx < PS * (K / 16); idx += blockDim.x) {
     const int sp = idx / (K / 16), c = idx % (K / 16);
     const int pr = a.sorted[sp], tok = pr < P ? pr / a.k : pr - P;

@@ -220,7 +220,8 @@ class Engine:
         if cfg.arch == "deepseek2":
             return Engine._deepseek_from_gguf(m, cfg, path, device, max_batch, tp_rank, tp_world, ph, timing,
                                               **{k: v for k, v in kw.items()
-                                                 if k in ("block_size", "num_blocks", "kv_fraction", "policy")})
+                                                 if k in ("block_size", "num_blocks", "kv_fraction", "policy",
+                                                          "prefill_rows")})
         t = time.perf_counter()
         w = load_llama_weights(m, cfg, device)
         if quant_tier_map:

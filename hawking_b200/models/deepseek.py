@@ -267,10 +267,22 @@ class DeepSeekModel:
         ops.launches.add(4)
         K.mla_kv_append(self.kva[:rows], L.kv_a_norm, cfg.eps, inp.positions[:rows], kv.block_tables,
                         inp.row_seq[:rows], self.rope, kv.latent[l], ops.PDL)
-        for c0 in range(0, rows, 8):  # the absorb kernel takes up to 8 rows
-            c1 = min(rows, c0 + 8)
-            K.mla_absorb_q(self.q[c0:c1], L.w_uk, inp.positions[c0:c1], self.rope, self.q_lat[c0:c1],
-                           self.q_pe[c0:c1], ops.PDL)
+        if wide:
+            # key absorption of every head as one batched bf16 GEMM, and the query RoPE (halves)
+            nh, nope = cfg.n_heads, cfg.qk_nope_dim
+            qv = self.q[:rows].view(rows, nh, nope + ROPE)
+            ql = torch.bmm(qv[:, :, :nope].transpose(0, 1).to(torch.bfloat16), L.w_uk)  # [nh, rows, 512]
+            self.q_lat[:rows].copy_(ql.transpose(0, 1))
+            cs = self.rope[inp.positions[:rows].long()]                                 # [rows, 32, 2]
+            c, sn = cs[:, None, :, 0], cs[:, None, :, 1]
+            a, b = qv[:, :, nope:nope + ROPE // 2], qv[:, :, nope + ROPE // 2:]
+            self.q_pe[:rows, :, :ROPE // 2] = a * c - b * sn
+            self.q_pe[:rows, :, ROPE // 2:] = b * c + a * sn
+        else:
+            for c0 in range(0, rows, 8):  # the absorb kernel takes up to 8 rows
+                c1 = min(rows, c0 + 8)
+                K.mla_absorb_q(self.q[c0:c1], L.w_uk, inp.positions[c0:c1], self.rope, self.q_lat[c0:c1],
+                               self.q_pe[c0:c1], ops.PDL)
         # num_splits 0: the tensor-core kernel (mla_flash.cu, picks its own splits) for 4+ rows, where it
         # measured 2.4x faster at 8 rows; fewer rows stay on the CUDA-core kernel (as fast at 64 heads,
         # faster for tensor-parallel head shards)
@@ -278,15 +290,19 @@ class DeepSeekModel:
         K.mla_decode(self.q_lat[:rows], self.q_pe[:rows], kv.latent[l], kv.block_tables, inp.row_seq[:rows],
                      inp.row_ctx[:rows], self.scale, 0 if flash else self.num_splits(rows),
                      self.o_lat[:rows], self.status, ops.PDL)
+        if wide:
+            # value up-projection of every head as one batched bf16 GEMM, straight to the bf16 rows
+            # of the O GEMM (no int8 round trip)
+            nh, vd = cfg.n_heads, cfg.v_head_dim
+            o = torch.bmm(self.o_lat[:rows].transpose(0, 1).to(torch.bfloat16), L.w_uv.transpose(1, 2))
+            self.attb[:rows].view(rows, nh, vd).copy_(o.transpose(0, 1))
+            self.wide.linear(L.idx["o"], self.attb[:rows], self.x[:rows], residual=True)
+            return
         for c0 in range(0, rows, 8):
             c1 = min(rows, c0 + 8)
             K.mla_out(self.o_lat[c0:c1], L.w_uv, self.attq.q[c0:c1], self.attq.d[c0:c1], self.attq.s[c0:c1], ops.PDL)
         if self.tp is not None:
             mixed_gemv_push(t, L.idx["o"], self.attq.view(rows), self.tp, 2 * l)
-        elif wide:
-            from ..ops.prefill import q8_to_bf16
-            q8_to_bf16(self.attq.view(rows), self.attb[:rows])
-            self.wide.linear(L.idx["o"], self.attb[:rows], self.x[:rows], residual=True)
         else:
             mixed_gemv(t, L.idx["o"], self.attq.view(rows), self.x[:rows], residual=True)
 
@@ -374,7 +390,7 @@ class DeepSeekModel:
         ops.router_logits(L.router, xa, self.rlog[:rows])
         ops.moe_topk(self.rlog[:rows], L.router_bias, k, self.scoring, cfg.n_groups, cfg.topk_groups, cfg.norm_topk,
                      cfg.routed_scale, self.ids[:rows], self.rw[:rows])
-        ops.moe_align(self.ids[:rows], E, xa, self.counts, self.offsets, self.sorted, self.gx, shared=fold)
+        ops.moe_align(self.ids[:rows], E, xa, self.counts, self.offsets, self.sorted, None, shared=fold)
         self.prefill.run(L.idx, rows, k, self.xb[:rows], self.x[:rows], self.counts, self.offsets, self.sorted,
                          self.rw[:rows], fold, pdl=ops.PDL)
         if not fold and "sg" in L.idx:

@@ -380,7 +380,7 @@ class QwenNextModel:
             ops.rmsnorm(self.x[:rows], L.post_norm, cfg.eps, yb=self.xb[:rows])
             ops.router_logits(L.router, xa, self.rlog[:rows])
             ops.moe_topk(self.rlog[:rows], None, k, 0, 1, 1, cfg.norm_topk, 1.0, self.ids[:rows], self.rw[:rows])
-            ops.moe_align(self.ids[:rows], E, xa, self.counts, self.offsets, self.sorted, self.gx, shared=True)
+            ops.moe_align(self.ids[:rows], E, xa, self.counts, self.offsets, self.sorted, None, shared=True)
             self.prefill.run(L.idx, rows, k, self.xb[:rows], self.x[:rows], self.counts, self.offsets, self.sorted,
                              self.rw[:rows], True, shared_gate=self.sglog[:rows], pdl=ops.PDL)
             return

@@ -312,10 +312,15 @@ def moe_route(router, x: Q8Act, k: int, scoring: int, bias, n_groups: int, topk_
                         e_lo=e_lo, e_hi=e_hi)
 
 
-def moe_align(ids, E: int, x: Q8Act, counts, offsets, sorted_pairs, gathered: Q8Act, shared: bool = False):
-    """Counting sort of the (token, expert) pairs by expert plus the gather of their q8 rows;
-    ``shared`` appends expert E (a shared expert) with one pair per token after the routed ones."""
+def moe_align(ids, E: int, x: Q8Act, counts, offsets, sorted_pairs, gathered: Optional[Q8Act], shared: bool = False):
+    """Counting sort of the (token, expert) pairs by expert plus the gather of their q8 rows
+    (``gathered`` None: the sort only); ``shared`` appends expert E (a shared expert) with one pair
+    per token after the routed ones."""
     launches.add()
+    if gathered is None:
+        e8, ef = torch.empty(0, dtype=torch.int8, device=ids.device), torch.empty(0, device=ids.device)
+        kernels().moe_align(ids, E, x.q, x.d, x.s, counts, offsets, sorted_pairs, e8, ef, ef, PDL, shared)
+        return
     kernels().moe_align(ids, E, x.q, x.d, x.s, counts, offsets, sorted_pairs, gathered.q, gathered.d, gathered.s, PDL,
                         shared)
 

