@@ -85,8 +85,105 @@ __global__ void __launch_bounds__(256) deltanet_conv_kernel(DeltaConvArgs a) {
   pdl_launch();
 }
 
+// ---- wide forwards (prefill): every row's convolution in parallel ----------------------------
+// Input j steps back from row r (j = 0: row r itself): a row of the same run while j <= back (the
+// run's rows before r, at most kc - 1 looked at), else the (j - back)-th newest entry of the
+// sequence's conv state (entries oldest first). The state is only read here; the rows that end a
+// run write their sequence's new state in deltanet_conv_state_kernel afterwards.
+struct ConvIn {
+  const DeltaConvArgs& a;
+  int r, kh, back, ch_total;
+  const float* cst;
+  __device__ __forceinline__ float at(int ch, int col, int j) const {
+    if (j <= back) return a.qkvz[(int64_t)(r - j) * a.qkvz_stride + (int64_t)kh * (2 * a.dk + 2 * a.r * a.dv) + col];
+    return cst[(int64_t)ch * (a.kc - 1) + (a.kc - 1) - (j - back)];
+  }
+};
+
+__device__ __forceinline__ int conv_back(const DeltaConvArgs& a, int r, int slot) {
+  int back = 0;
+  if (a.state_slot)
+    while (back < a.kc - 1 && r - back - 1 >= 0 && a.state_slot[r - back - 1] == slot) ++back;
+  return back;
+}
+
+__global__ void __launch_bounds__(256) deltanet_conv_wide_kernel(DeltaConvArgs a) {
+  __shared__ float red[2][8];
+  pdl_wait();
+  const int kh = blockIdx.x, r = blockIdx.y, tid = threadIdx.x;
+  const int dk = a.dk, rv = a.r * a.dv;
+  const int key_elems = a.kh * dk;
+  const int ch_total = 2 * key_elems + a.kh * rv;
+  const int slot = a.state_slot ? a.state_slot[r] : r;
+  const ConvIn in{a, r, kh, conv_back(a, r, slot), ch_total,
+                  a.conv_state + (int64_t)slot * ch_total * (a.kc - 1)};
+  auto conv = [&](int ch, int col) {
+    const float* w = a.conv_w + (int64_t)ch * a.kc;
+    float s = 0.f;
+    for (int j = 0; j < a.kc; ++j) s += w[a.kc - 1 - j] * in.at(ch, col, j);
+    return s / (1.f + __expf(-s));
+  };
+  const float* row = a.qkvz + (int64_t)r * a.qkvz_stride + (int64_t)kh * (2 * dk + 2 * rv);
+  float qv = 0.f, kv = 0.f;
+  if (tid < dk) {
+    qv = conv(kh * dk + tid, tid);
+    kv = conv(key_elems + kh * dk + tid, dk + tid);
+  }
+  for (int i = tid; i < rv; i += blockDim.x) {
+    const int vh = kh * a.r + i / a.dv, d = i % a.dv;
+    a.v[(int64_t)r * a.kh * rv + (int64_t)vh * a.dv + d] = conv(2 * key_elems + kh * rv + i, 2 * dk + i);
+    a.z[(int64_t)r * a.kh * rv + (int64_t)vh * a.dv + d] = row[2 * dk + rv + i];
+  }
+  float sq = warp_sum(qv * qv), sk = warp_sum(kv * kv);
+  if ((tid & 31) == 0) { red[0][tid >> 5] = sq; red[1][tid >> 5] = sk; }
+  __syncthreads();
+  if (tid < dk) {
+    float tq = 0.f, tk = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) { tq += red[0][w]; tk += red[1][w]; }
+    const float qs = rsqrtf(tq + a.eps) * rsqrtf((float)dk), ks = rsqrtf(tk + a.eps);
+    for (int j = 0; j < a.r; ++j) {
+      const int vh = kh * a.r + j;
+      a.q[((int64_t)r * a.kh * a.r + vh) * dk + tid] = qv * qs;
+      a.k[((int64_t)r * a.kh * a.r + vh) * dk + tid] = kv * ks;
+    }
+  }
+  pdl_launch();
+}
+
+// The rows that end a run: the sequence's conv state becomes the run's last kc - 1 inputs (older
+// state entries where the run is shorter). Each thread reads its channels' values, then writes.
+__global__ void __launch_bounds__(256) deltanet_conv_state_kernel(DeltaConvArgs a, int rows) {
+  pdl_wait();
+  const int kh = blockIdx.x, r = blockIdx.y, tid = threadIdx.x;
+  const int slot = a.state_slot ? a.state_slot[r] : r;
+  const bool last = r == rows - 1 || !a.state_slot || a.state_slot[r + 1] != slot;
+  if (last) {
+    const int dk = a.dk, rv = a.r * a.dv;
+    const int key_elems = a.kh * dk;
+    const int ch_total = 2 * key_elems + a.kh * rv;
+    float* cst = a.conv_state + (int64_t)slot * ch_total * (a.kc - 1);
+    const ConvIn in{a, r, kh, conv_back(a, r, slot), ch_total, cst};
+    auto update = [&](int ch, int col) {
+      float v[8];
+      for (int t = 0; t < a.kc - 1; ++t) v[t] = in.at(ch, col, a.kc - 2 - t);
+      for (int t = 0; t < a.kc - 1; ++t) cst[(int64_t)ch * (a.kc - 1) + t] = v[t];
+    };
+    if (tid < dk) {
+      update(kh * dk + tid, tid);
+      update(key_elems + kh * dk + tid, dk + tid);
+    }
+    for (int i = tid; i < rv; i += blockDim.x) update(2 * key_elems + kh * rv + i, 2 * dk + i);
+  }
+  pdl_launch();
+}
+
 void deltanet_conv_launch(const DeltaConvArgs& a, int rows, cudaStream_t s, bool pdl) {
   if (a.dk > 256 || a.dk % 32) throw std::runtime_error("deltanet: key head dim must be a multiple of 32, <= 256");
+  if (rows > 8 && a.kc <= 9) {  // prefill-sized forwards: every row in parallel, then the states
+    launch(deltanet_conv_wide_kernel, dim3(a.kh, rows), dim3(256), 0, s, pdl, a);
+    launch(deltanet_conv_state_kernel, dim3(a.kh, rows), dim3(256), 0, s, pdl, a, rows);
+    return;
+  }
   launch(deltanet_conv_kernel, dim3(a.kh, rows), dim3(256), 0, s, pdl, a);
 }
 

@@ -80,3 +80,41 @@ def test_qwen_next_wide_components_match_torch():
                 W[L.idx["sd"]] @ (silu(W[L.idx["sg"]] @ xn[t]) * (W[L.idx["su"]] @ xn[t])))
         err = (got - ref).abs().amax(1) / ref.abs().max()
         assert (err < 2e-2).float().mean().item() >= 0.9, err.tolist()
+
+
+def test_deltanet_conv_wide_matches_walk():
+    """The parallel convolution of a wide forward (two runs of 13 and 20 rows, each continuing a
+    sequence whose conv state holds earlier inputs) equals the token walk run in forwards of up to
+    8 rows: outputs and the final conv states."""
+    from hawking_b200._ext import kernels
+    kh, r, dk, dv, kc = 2, 2, 64, 64, 4
+    ch = 2 * kh * dk + kh * r * dv
+    qkvz_w = 2 * kh * dk + 2 * kh * r * dv
+    g = torch.Generator(device=DEV).manual_seed(9)
+    lens = [13, 20]
+    rows = sum(lens)
+    qkvz = torch.randn(rows, qkvz_w, generator=g, device=DEV)
+    conv_w = torch.randn(ch, kc, generator=g, device=DEV) * 0.3
+    state0 = torch.randn(3, ch, kc - 1, generator=g, device=DEV)
+    slot = torch.tensor([1] * lens[0] + [2] * lens[1], dtype=torch.int32, device=DEV)
+
+    def outs(n):
+        return (torch.zeros(n, kh * r, dk, device=DEV), torch.zeros(n, kh * r, dk, device=DEV),
+                torch.zeros(n, kh * r * dv, device=DEV), torch.zeros(n, kh * r * dv, device=DEV))
+
+    st_w = state0.clone()
+    qw, kw, vw, zw = outs(rows)
+    kernels().deltanet_conv(qkvz, conv_w, st_w, slot, kh, r, dk, dv, kc, 1e-6, qw, kw, vw, zw, False)
+    st_n = state0.clone()
+    qn, kn, vn, zn = outs(rows)
+    c0 = 0
+    for L in lens:
+        for a in range(c0, c0 + L, 8):
+            b = min(c0 + L, a + 8)
+            q1, k1, v1, z1 = outs(b - a)
+            kernels().deltanet_conv(qkvz[a:b], conv_w, st_n, slot[a:b], kh, r, dk, dv, kc, 1e-6, q1, k1, v1, z1, False)
+            qn[a:b], kn[a:b], vn[a:b], zn[a:b] = q1, k1, v1, z1
+        c0 += L
+    torch.cuda.synchronize()
+    for got, ref in ((qw, qn), (kw, kn), (vw, vn), (zw, zn), (st_w, st_n)):
+        assert (got - ref).abs().max().item() <= 1e-5 * (ref.abs().max().item() + 1), (got - ref).abs().max().item()
