@@ -79,7 +79,7 @@ struct TcArgs {
 };
 
 template <int HD, int NC>
-__global__ void __launch_bounds__(Cfg<NC>::kThreads, 1)
+__global__ void __launch_bounds__(Cfg<NC>::kThreads, 2)
     attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv, TcArgs a) {
   constexpr int kConsumers = Cfg<NC>::kConsumers, kThreads = Cfg<NC>::kThreads;
   constexpr int NKS = HD / 16;   // k-steps of S = Q K^T
@@ -403,7 +403,10 @@ void launch_hd_nc(const AttnDecodeArgs& a, int64_t cache_rows, cudaStream_t s, b
     const char* e = getenv("HK_ATTN_STAGES");
     return e && atoi(e) == 2 ? 2 : kStages;
   }();
-  t.stages = a.block_size == 16 ? kStages : env_stages;
+  // Many CTAs (wide decode batches): a 2-stage ring lets several CTAs share an SM, which matters
+  // more than ring depth once the launch has more than one wave; few CTAs keep 4 stages.
+  const bool many = (int64_t)a.num_splits * a.nkv * a.R > 148;
+  t.stages = a.block_size == 16 ? kStages : (many ? 2 : env_stages);
   const size_t smem = 1024 + (size_t)t.stages * 2 * a.block_size * HD * 2;
   auto kern = attn_decode_tc_kernel<HD, NC>;
   HK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));

@@ -1074,7 +1074,9 @@ void tc_gemm_bf16_launch(const TcBf16Args& g, cudaStream_t s) {
 int tc_gemm_splits(int N, int M, int K, int bn, int sms) {
   const int tiles = (N / BM) * ((M + bn - 1) / bn);
   const int stages = K / BK;
-  int splits = (sms + tiles - 1) / tiles;
+  // one CTA fills an SM (shared memory): as many splits as keep the launch within one wave, since
+  // a partial second wave costs a whole K slice (48 tiles: 3 splits / 144 CTAs, not 4 / 192)
+  int splits = tiles >= sms ? 1 : sms / tiles;
   splits = std::min(splits, std::max(1, stages / 4));  // keep >= 4 stages per split
   return std::max(1, splits);
 }

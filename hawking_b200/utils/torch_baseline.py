@@ -75,6 +75,9 @@ class TorchLlamaTP:
         return n + self.lm_head.numel() * 2
 
     def _rms(self, x, w):
+        # fused RMSNorm where PyTorch has one (fp32 statistics inside)
+        if hasattr(F, "rms_norm"):
+            return F.rms_norm(x, (x.shape[-1],), w, self.cfg.eps)
         xf = x.float()
         return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.cfg.eps)).to(x.dtype) * w
 
@@ -106,11 +109,9 @@ class TorchLlamaTP:
             if causal:  # prefill: fused SDPA (flash) with grouped heads
                 o = F.scaled_dot_product_attention(q, kk, vv, is_causal=True, enable_gqa=True,
                                                    scale=1.0 / math.sqrt(hd))
-            else:  # decode (T = 1): grouped-query batched GEMMs over the masked cache
-                G = self.lnh // self.lnkv
-                qg = q.reshape(B, self.lnkv, G, hd)
-                s = (qg @ kk.transpose(-1, -2)).float() * (1.0 / math.sqrt(hd)) + mask
-                o = (torch.softmax(s, -1).to(vv.dtype) @ vv).reshape(B, self.lnh, 1, hd)
+            else:  # decode (T = 1): SDPA over the masked cache (grouped heads)
+                o = F.scaled_dot_product_attention(q, kk, vv, attn_mask=mask, enable_gqa=True,
+                                                   scale=1.0 / math.sqrt(hd))
             o = o.transpose(1, 2).reshape(B, T, self.lnh * hd)
             x = x + self._allreduce(o @ L.wo.t())
             h = self._rms(x, L.ffn_norm)
@@ -150,8 +151,8 @@ class TorchLlamaTP:
         x = self.embed[self.ids].unsqueeze(1)
         pos = self.pos.unsqueeze(1)
         ar = torch.arange(self.cap, device=self.dev)
-        mask = torch.where(ar[None, :] <= self.pos[:, None], 0.0, float("-inf"))
-        mask = mask[:, None, None, :]  # [B, 1, 1, cap] fp32
+        mask = torch.where(ar[None, :] <= self.pos[:, None], 0.0, float("-inf")).to(torch.bfloat16)
+        mask = mask[:, None, None, :]  # [B, 1, 1, cap] additive
         bidx = torch.arange(B, device=self.dev)
 
         def write(l, k, v):
