@@ -785,13 +785,17 @@ def main():
         "higher_is_better": True,
         "scaling": "strong" if args.parallel == "tp" else "weak",
         "vs_baseline": None,
-        "dtype": ("q4_k weights, bf16 activations (W4A16 tensor-core GEMV), fp32 accumulate, bf16 KV"
-                  if m.small_batch == "w4a16" else
-                  "q4_k weights, int8 activation blocks (W4A8 dp4a), fp32 accumulate, bf16 KV"),
-        "data": "synthetic: random-init N(0,0.02) weights quantised to GGUF Q4_K on device; uniform-random "
-                "token ids; device-timed decode runs over a 2048-token KV context filled with random bf16",
-        "config": {"model": "llama3-8b (Llama-3-8B-arch: 32 layers, hidden 4096, 32/8 GQA heads, head_dim 128, "
-                            "FFN 14336, vocab 128256, rope theta 5e5, GGUF Q4_K)" + (
+        "dtype": (f"{cfg.weight_type.lower()} weights, bf16 activations (W4A16 tensor-core GEMV), fp32 accumulate, "
+                  "bf16 KV" if m.small_batch == "w4a16" and args.model == "llama3-8b" else
+                  f"{cfg.weight_type.lower()} weights, int8 activation blocks (dp4a GEMV), fp32 accumulate, bf16 KV"),
+        "data": f"synthetic: random-init N(0,0.02) weights quantised to GGUF {cfg.weight_type} on device; "
+                "uniform-random token ids; device-timed decode runs over a 2048-token KV context filled with "
+                "random bf16",
+        "config": {"model": (("llama3-8b (Llama-3-8B-arch: 32 layers, hidden 4096, 32/8 GQA heads, head_dim 128, "
+                              "FFN 14336, vocab 128256, rope theta 5e5, GGUF Q4_K)") if args.model == "llama3-8b" else
+                             f"{args.model} ({cfg.layers} layers, hidden {cfg.hidden}, {cfg.n_heads}/{cfg.n_kv_heads} "
+                             f"GQA heads, {cfg.n_experts} experts top-{cfg.top_k}, expert FFN {cfg.expert_ffn}, "
+                             f"vocab {cfg.vocab}, GGUF {cfg.weight_type})") + (
                                 f" [LAYERS OVERRIDDEN to {cfg.layers}]" if args.layers else ""),
                    "global_batch": B * replicas, "seq_len": ctx,
                    "parallelism": f"tp{world}" if use_tp else (f"dp{world}" if world > 1 else "tp1"),

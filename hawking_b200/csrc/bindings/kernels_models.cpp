@@ -209,6 +209,22 @@ void moe_combine(const Tensor& y, const Tensor& pos, const Tensor& w, int64_t T,
                          x.data_ptr<float>(), x.stride(0), (int)x.size(1), cur_stream(), pdl);
 }
 
+void qweight_dequant_bf16(int64_t fmt, const std::vector<Tensor>& planes, int64_t K, int64_t group_rows,
+                          int64_t dst_group_rows, int64_t dst_off, const Tensor& out, bool pdl) {
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.stride(-1) == 1, "qweight_dequant_bf16: bf16 rows");
+  TORCH_CHECK(!planes.empty() && planes.size() <= 4, "qweight_dequant_bf16: 1-4 planes");
+  hk::WPlanes w{};
+  const uint8_t** p[4] = {&w.p0, &w.p1, &w.p2, &w.p3};
+  int64_t* rb[4] = {&w.rb0, &w.rb1, &w.rb2, &w.rb3};
+  for (size_t i = 0; i < planes.size(); ++i) {
+    *p[i] = reinterpret_cast<const uint8_t*>(planes[i].data_ptr());
+    *rb[i] = planes[i].stride(0);
+  }
+  const c10::cuda::CUDAGuard g(out.device());
+  hk::qweight_dequant_bf16_launch((int)fmt, w, (int)planes[0].size(0), (int)K, (int)group_rows, (int)dst_group_rows,
+                                  (int)dst_off, bfpm(out), out.stride(0), cur_stream(), pdl);
+}
+
 void q8_to_bf16(const Tensor& q, const Tensor& d, const Tensor& out, bool pdl) {
   const c10::cuda::CUDAGuard g(q.device());
   hk::q8_to_bf16_launch(q.data_ptr<int8_t>(), d.data_ptr<float>(), q.stride(0), d.stride(0), (int)q.size(0),
@@ -511,6 +527,8 @@ void register_model_kernels(py::module_& m) {
         py::arg("x"), py::arg("xg"), py::arg("pos"), py::arg("pdl") = false);
   m.def("moe_combine", &moe_combine, py::arg("y"), py::arg("pos"), py::arg("w"), py::arg("T"), py::arg("k"),
         py::arg("shared"), py::arg("shared_gate"), py::arg("x"), py::arg("pdl") = false);
+  m.def("qweight_dequant_bf16", &qweight_dequant_bf16, py::arg("fmt"), py::arg("planes"), py::arg("K"),
+        py::arg("group_rows"), py::arg("dst_group_rows"), py::arg("dst_off"), py::arg("out"), py::arg("pdl") = false);
   m.def("q8_to_bf16", &q8_to_bf16, py::arg("q"), py::arg("d"), py::arg("out"), py::arg("pdl") = false);
   m.def("mixed_descs", &mixed_descs, py::arg("codes"), py::arg("scales"), py::arg("kind"), py::arg("bits"),
         py::arg("group"), py::arg("zeros") = std::vector<int64_t>{});

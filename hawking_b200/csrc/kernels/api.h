@@ -566,6 +566,8 @@ void moe_gather_bf16_launch(const int* sorted, int PS, int P, int k, const __nv_
 void moe_combine_launch(const float* y, int64_t y_stride, const int* pos, const float* w, int T, int k, bool shared,
                         const float* shared_gate, int64_t gate_stride, float* x, int64_t x_stride, int H,
                         cudaStream_t s, bool pdl);
+void qweight_dequant_bf16_launch(int fmt, const WPlanes& w, int rows, int K, int group_rows, int dst_group_rows,
+                                 int dst_off, __nv_bfloat16* out, int64_t out_stride, cudaStream_t s, bool pdl);
 void q8_to_bf16_launch(const int8_t* q, const float* d, int64_t q_stride, int64_t d_stride, int rows, int K,
                        __nv_bfloat16* out, int64_t out_stride, cudaStream_t s, bool pdl);
 // HGRAVR02 outlier residual added into y [nb, >= N] (row_ptr [N + 1], cols / signs [nnz]).

@@ -415,8 +415,9 @@ void launch_hd_nc(const AttnDecodeArgs& a, int64_t cache_rows, cudaStream_t s, b
 
 template <int HD>
 void launch_hd(const AttnDecodeArgs& a, int64_t cache_rows, cudaStream_t s, bool pdl) {
-  // 4 consumers at every block size: 8 (sound for blocks of 32 / 64) measured slower at Llama-3-8B
-  // decode shapes (12.4 vs 10.6 us per layer; the fold into shared memory doubles)
+  // 4 consumers: 8 (sound for blocks of 32 / 64) measured slower both at Llama-3-8B bs1 decode
+  // shapes (12.4 vs 10.6 us per layer; the fold into shared memory doubles) and at bs64
+  // (187 vs 135 us per layer); 2 splits at bs64 measured slower too (153 us)
   launch_hd_nc<HD, 4>(a, cache_rows, s, pdl);
 }
 

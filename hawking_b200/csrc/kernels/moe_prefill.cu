@@ -99,6 +99,91 @@ void mixed_dequant_bf16_launch(const MixedDesc* desc, const int* didx, const int
   launch(mixed_dequant_bf16_kernel, dim3(rows, count), dim3(128), 0, s, pdl, desc, didx, drow, K, out, out_stride);
 }
 
+// ---- GGUF block formats -> bf16 (the stacked expert matrices of the GGUF MoE models) -----------
+// Value i (0..31) of 32-element block b of row r, from the planes of a re-laid GGUF tensor (each
+// plane holds one byte range of every block; api.h WPlanes). The formulas are the GGUF formats'.
+__device__ __forceinline__ void gguf_block_values(int fmt, const WPlanes& w, int64_t r, int b, float (&v)[32]) {
+  if (fmt == WF_Q8_0) {
+    const int8_t* q = reinterpret_cast<const int8_t*>(w.p0 + r * w.rb0 + (int64_t)b * 32);
+    const float d = __half2float(*reinterpret_cast<const __half*>(w.p1 + r * w.rb1 + (int64_t)b * 2));
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = d * (float)q[i];
+  } else if (fmt == WF_Q4_0 || fmt == WF_Q5_0) {
+    const uint8_t* q = w.p0 + r * w.rb0 + (int64_t)b * 16;
+    const float d = __half2float(*reinterpret_cast<const __half*>(w.p1 + r * w.rb1 + (int64_t)b * 2));
+    uint32_t qh = 0;
+    if (fmt == WF_Q5_0) {
+      const uint8_t* h = w.p2 + r * w.rb2 + (int64_t)b * 4;
+      qh = (uint32_t)h[0] | ((uint32_t)h[1] << 8) | ((uint32_t)h[2] << 16) | ((uint32_t)h[3] << 24);
+    }
+    const int off = fmt == WF_Q5_0 ? 16 : 8;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      int n = i < 16 ? (q[i] & 0xF) : (q[i - 16] >> 4);
+      if (fmt == WF_Q5_0) n |= ((qh >> i) & 1u) << 4;
+      v[i] = d * (float)(n - off);
+    }
+  } else if (fmt == WF_Q4_K) {
+    const int sb = b >> 3, j = b & 7;
+    const uint4 h = *reinterpret_cast<const uint4*>(w.p1 + r * w.rb1 + (int64_t)sb * 16);
+    int sc, mn;
+    q4k_scale_min(j, h.y, h.z, h.w, sc, mn);
+    const float d = __half2float(__ushort_as_half((unsigned short)(h.x & 0xFFFFu)));
+    const float dmin = __half2float(__ushort_as_half((unsigned short)(h.x >> 16)));
+    const uint8_t* q = w.p0 + r * w.rb0 + (int64_t)sb * 128 + (j >> 1) * 32;
+    const int sh = (j & 1) * 4;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = d * (float)sc * (float)((q[i] >> sh) & 0xF) - dmin * (float)mn;
+  } else {  // Q6_K: 32-element quarter qd of half n of super-block sb
+    const int sb = b >> 3, j = b & 7, n = j >> 2, qd = j & 3;
+    const uint8_t* ql = w.p0 + r * w.rb0 + (int64_t)sb * 128 + 64 * n + (qd & 1) * 32;
+    const uint8_t* qh = w.p1 + r * w.rb1 + (int64_t)sb * 64 + 32 * n;
+    const int8_t* sc = reinterpret_cast<const int8_t*>(w.p2 + r * w.rb2 + (int64_t)sb * 16 + 8 * n);
+    const float d = __half2float(*reinterpret_cast<const __half*>(w.p3 + r * w.rb3 + (int64_t)sb * 2));
+#pragma unroll
+    for (int l = 0; l < 32; ++l) {
+      const int nib = qd < 2 ? (ql[l] & 0xF) : (ql[l] >> 4);
+      const int q = (nib | (((qh[l] >> (2 * qd)) & 3) << 4)) - 32;
+      v[l] = d * (float)sc[l / 16 + 2 * qd] * (float)q;
+    }
+  }
+}
+
+// grid (rows): source row r of a stacked [groups * group_rows, K] tensor -> out row
+// (r / group_rows) * dst_group_rows + dst_off + r % group_rows.
+__global__ void __launch_bounds__(128) qweight_dequant_bf16_kernel(int fmt, WPlanes w, int K, int group_rows,
+                                                                   int dst_group_rows, int dst_off,
+                                                                   __nv_bfloat16* out, int64_t out_stride) {
+  pdl_wait();
+  const int r = blockIdx.x;
+  const int64_t dr = (int64_t)(r / group_rows) * dst_group_rows + dst_off + r % group_rows;
+  __nv_bfloat16* o = out + dr * out_stride;
+  for (int b = threadIdx.x; b < K / 32; b += blockDim.x) {
+    float v[32];
+    gguf_block_values(fmt, w, r, b, v);
+    uint4* dst = reinterpret_cast<uint4*>(o + b * 32);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      __nv_bfloat162 p[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) p[e] = __floats2bfloat162_rn(v[8 * c + 2 * e], v[8 * c + 2 * e + 1]);
+      dst[c] = *reinterpret_cast<uint4*>(p);
+    }
+  }
+  pdl_launch();
+}
+
+void qweight_dequant_bf16_launch(int fmt, const WPlanes& w, int rows, int K, int group_rows, int dst_group_rows,
+                                 int dst_off, __nv_bfloat16* out, int64_t out_stride, cudaStream_t s, bool pdl) {
+  if (fmt != WF_Q8_0 && fmt != WF_Q4_0 && fmt != WF_Q5_0 && fmt != WF_Q4_K && fmt != WF_Q6_K)
+    throw std::runtime_error("qweight dequant: Q8_0, Q4_0, Q5_0, Q4_K or Q6_K");
+  if (K % ((fmt == WF_Q4_K || fmt == WF_Q6_K) ? 256 : 32) || out_stride % 8)
+    throw std::runtime_error("qweight dequant: K must be whole blocks, rows 16-byte aligned");
+  if (rows <= 0) return;
+  launch(qweight_dequant_bf16_kernel, dim3(rows), dim3(128), 0, s, pdl, fmt, w, K, group_rows, dst_group_rows,
+         dst_off, out, out_stride);
+}
+
 // Tiles of bn pairs per expert from the counting sort (one CTA; E1 <= 1024).
 __global__ void __launch_bounds__(1024) moe_tiles_kernel(const int* counts, const int* offsets, int E1, int bn,
                                                          int* tiles, int* n_tiles) {

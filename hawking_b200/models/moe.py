@@ -25,6 +25,11 @@ from ..ops import Q8Act, QWeight, cat_rows
 from .config import ModelConfig
 
 
+# forwards of more than 8 rows on one GPU run the experts as grouped tensor-core GEMMs over bf16
+# copies of their weights (0: the GEMV kernels)
+WIDE_MOE = __import__("os").environ.get("HK_MOE_PREFILL", "1") == "1"
+
+
 @dataclass
 class MoEFFN:
     cfg: ModelConfig
@@ -90,6 +95,14 @@ class MoEFFN:
         else:
             self.sh_gate, self.sh_up = g, u
         self.sh_down = d
+
+    def _wide(self, model, rows: int) -> bool:
+        """This forward's experts run as grouped tensor-core GEMMs (prefill-sized, one GPU)."""
+        from ..ops.prefill import GGUF_DEQUANT
+        cfg = self.cfg
+        return (WIDE_MOE and rows > 8 and getattr(model, "tp", None) is None and not self.n_local and
+                cfg.expert_ffn % 128 == 0 and cfg.hidden % 128 == 0 and
+                all(w.fmt in GGUF_DEQUANT for w in (self.w_gate, self.w_up, self.w_down)))
 
     # ---- buffers (per model, sized for max rows) ----
     def _buffers(self, model):
@@ -207,11 +220,26 @@ class MoEFFN:
         ops.moe_topk(b["logits"][:rows], self.router_bias, k, scoring, cfg.n_groups if scoring else 1,
                      cfg.topk_groups if scoring else 1, cfg.norm_topk, cfg.routed_scale, b["ids"][:rows],
                      b["weights"][:rows])
-        ops.moe_align(b["ids"][:rows], E, xa, b["counts"], b["offsets"], b["sorted"], b["gx"])
-        ops.moe_gemv_swiglu(self.w_gate, self.w_up, Fe, E, k, b["counts"], b["offsets"], b["sorted"], b["gx"],
-                            b["h"])
-        ops.moe_gemv_down(self.w_down, H, E, k, b["counts"], b["offsets"], b["sorted"], b["h"], x,
-                          b["weights"][:rows].reshape(-1))
+        if self._wide(model, rows):
+            # prefill: every expert decoded once into a bf16 copy, the pairs sorted by expert, and
+            # two grouped tensor-core GEMMs over them (ops/prefill.py)
+            from ..ops.prefill import MoePrefill, q8_to_bf16
+            ops.moe_align(b["ids"][:rows], E, xa, b["counts"], b["offsets"], b["sorted"], None)
+            pf = getattr(model, "_moe_prefill", None)
+            if pf is None:
+                pf = model._moe_prefill = MoePrefill(None, model.dev, E, Fe, H, model.max_rows * (k + 1),
+                                                     model.status)
+                model._moe_xb = torch.zeros(model.max_rows, H, dtype=torch.bfloat16, device=model.dev)
+            xb = model._moe_xb[:rows]
+            q8_to_bf16(xa, xb)
+            pf.run_gguf(self.w_gate, self.w_up, self.w_down, rows, k, xb, x, b["counts"], b["offsets"], b["sorted"],
+                        b["weights"][:rows], pdl=ops.PDL)
+        else:
+            ops.moe_align(b["ids"][:rows], E, xa, b["counts"], b["offsets"], b["sorted"], b["gx"])
+            ops.moe_gemv_swiglu(self.w_gate, self.w_up, Fe, E, k, b["counts"], b["offsets"], b["sorted"], b["gx"],
+                                b["h"])
+            ops.moe_gemv_down(self.w_down, H, E, k, b["counts"], b["offsets"], b["sorted"], b["h"], x,
+                              b["weights"][:rows].reshape(-1))
         if self.sh_down is not None:
             hs = b["hs"].view(rows)
             hs_v = model._q8_slice(b["hs"], 0, rows, self.sh_gate.N)

@@ -20,6 +20,7 @@ import torch
 from .._ext import kernels
 
 BN = 64  # pairs per grouped GEMM tile
+GGUF_DEQUANT = (2, 6, 8, 12, 14)  # GGUF formats the block decoder takes: Q4_0, Q5_0, Q8_0, Q4_K, Q6_K
 
 
 class MoePrefill:
@@ -66,10 +67,26 @@ class MoePrefill:
         K = kernels()
         gi, gr, di, dr, n = self._lists_for(idx, fold)
         F, H = self.F, self.H
-        P = rows * k
-        PS = P + (rows if fold else 0)
         K.mixed_dequant_bf16(self.table.descs, gi, gr, F, H, self.w_gu, pdl)
         K.mixed_dequant_bf16(self.table.descs, di, dr, H, F, self.w_dn, pdl)
+        self._experts(n, rows, k, xb, x, counts, offsets, sorted_pairs, route_w, fold, shared_gate, pdl)
+
+    def run_gguf(self, w_gate, w_up, w_down, rows: int, k: int, xb: torch.Tensor, x: torch.Tensor, counts,
+                 offsets, sorted_pairs, route_w, pdl: bool = False):
+        """The same for stacked GGUF expert tensors (QWeight [E F, H] gate / up, [E H, F] down): the
+        blocks are decoded into the bf16 copies by the GGUF-format kernel."""
+        K = kernels()
+        F, H = self.F, self.H
+        K.qweight_dequant_bf16(w_gate.fmt, w_gate.planes, H, F, 2 * F, 0, self.w_gu, pdl)
+        K.qweight_dequant_bf16(w_up.fmt, w_up.planes, H, F, 2 * F, F, self.w_gu, pdl)
+        K.qweight_dequant_bf16(w_down.fmt, w_down.planes, F, H, H, 0, self.w_dn, pdl)
+        self._experts(self.E, rows, k, xb, x, counts, offsets, sorted_pairs, route_w, False, None, pdl)
+
+    def _experts(self, n, rows, k, xb, x, counts, offsets, sorted_pairs, route_w, fold, shared_gate, pdl):
+        K = kernels()
+        F, H = self.F, self.H
+        P = rows * k
+        PS = P + (rows if fold else 0)
         K.moe_tiles(counts, offsets, n, BN, self.tiles, self.n_tiles, pdl)
         K.moe_gather_bf16(sorted_pairs, PS, P, k, xb, self.xg, self.pos, pdl)
         mt = (PS + BN - 1) // BN + n

@@ -108,3 +108,24 @@ def test_grouped_experts_pipeline():
             hh = (torch.nn.functional.silu(gu[:F]) * gu[F:]).bfloat16().float()
             ref[t] += rw[t, j] * (wdn[e * H:(e + 1) * H].float() @ hh)
     assert (x - ref).abs().max().item() <= 2e-2 * ref.abs().max().item()
+
+
+@pytest.mark.parametrize("fmt", [8, 2, 6, 12, 14])  # Q8_0, Q4_0, Q5_0, Q4_K, Q6_K
+def test_gguf_blocks_decode_to_bf16(fmt):
+    """GGUF planes of a stacked two-expert tensor -> bf16 rows in the [gate | up] per-expert layout
+    (gate rows at 2F e, up rows at 2F e + F), against the PyTorch restatement of the format."""
+    from hawking_b200.ops import QWeight
+    g = _g(fmt)
+    F, K = 64, 512
+    gate = QWeight.quantize(torch.randn(2 * F, K, generator=g, device=DEV) * 0.05, fmt)
+    up = QWeight.quantize(torch.randn(2 * F, K, generator=g, device=DEV) * 0.05, fmt)
+    out = torch.zeros(4 * F, K, dtype=torch.bfloat16, device=DEV)
+    kernels().qweight_dequant_bf16(gate.fmt, gate.planes, K, F, 2 * F, 0, out)
+    kernels().qweight_dequant_bf16(up.fmt, up.planes, K, F, 2 * F, F, out)
+    torch.cuda.synchronize()
+    gd, ud = gate.dequantize(), up.dequantize()
+    for e in range(2):
+        for src, off in ((gd, 0), (ud, F)):
+            ref = src[e * F:(e + 1) * F]
+            got = out[2 * F * e + off:2 * F * e + off + F].float()
+            assert (got - ref).abs().max().item() <= 8e-3 * ref.abs().max().item() + 1e-7, (fmt, e, off)
