@@ -104,6 +104,10 @@ class Engine:
         """``tp`` (parallel.tp.TPComm): ``cfg`` and ``weights`` are this rank's tensor-parallel shard."""
         from ..models.llama import LlamaModel
         max_ctx = max_ctx or cfg.max_ctx
+        if cfg.is_moe and tp is None:
+            # MoE prefill decodes every expert once per forward (grouped tensor-core GEMMs):
+            # prompts run in forwards of up to 2048 rows so that cost is shared by more tokens
+            max_prefill_tokens = max(max_prefill_tokens, 2048)
         bpb = PagedKVCache.bytes_per_block(cfg.layers, cfg.n_kv_heads, cfg.head_dim, block_size)
         free, _ = torch.cuda.mem_get_info(device)
         if num_blocks is None:

@@ -34,6 +34,9 @@ from .config import ModelConfig
 GEMV_COLS = 8  # rows per GEMV launch (dp4a GEMV batch limit)
 # RoPE + paged K/V append in the W4A16 QKV GEMV epilogue where the weights allow it
 ROPE_EPI = os.environ.get("HK_ROPE_EPI", "1") == "1"
+# prefill-sized forwards of GGUF formats other than Q4_K run their dense projections as tensor-core
+# GEMMs over bf16 copies of the weights (0: the dp4a GEMV)
+WIDE_GGUF = os.environ.get("HK_WIDE_GGUF", "1") == "1"
 
 
 @dataclass
@@ -542,9 +545,35 @@ class LlamaModel:
             mg.quantize(hb, nb, self.hfrag)
             mg.gemv(lw.mg_down, nb, xfrag=self.hfrag, status=st, **down_out)
 
+    def _wide_gguf(self, lw, rows) -> bool:
+        """Projections of this prefill-sized forward on the tensor cores over bf16 copies of the GGUF
+        weights (dense formats the tensor-core Q4_K GEMM does not take, e.g. Mixtral's Q8_0)."""
+        from ..ops.prefill import QWideLinear
+        # MoE layers only: their prefill already runs the experts wide; dense GGUF models keep the
+        # GEMV, whose rows do not depend on the batch they share (prefix reuse is exact)
+        if self.tp is not None or rows <= 32 or not WIDE_GGUF or lw.moe is None:
+            return False
+        ws = list(lw.wqkv) + [lw.wo]
+        if not all(QWideLinear.supports(w) for w in ws) or self.cfg.hidden % 128:
+            return False
+        if getattr(self, "_qwide", None) is None:
+            self._qwide = QWideLinear(self.dev, self.status)
+        return True
+
     def _attention_block_gemv(self, l, lw, rows, splits):
         x = self.x[:rows]
         ops.rmsnorm_q8(x, lw.attn_norm, self.cfg.eps, self.xa.view(rows))
+        if self._wide_gguf(lw, rows):
+            from ..ops.prefill import q8_to_bf16
+            q8_to_bf16(self.xa.view(rows), self.xb[:rows])
+            off = 0
+            for wt in lw.wqkv:
+                self._qwide.linear(wt, self.xb[:rows], self.qkv[:rows, off:off + wt.N])
+                off += wt.N
+            self._rope_attention(l, lw, rows, splits, out_q8=self.att.view(rows))
+            q8_to_bf16(self.att.view(rows), self.attb[:rows])
+            self._qwide.linear(lw.wo, self.attb[:rows], x, residual=True)
+            return
 
         def qkv_fn(c0, c1):
             xa = self.xa_view(c0, c1)

@@ -165,3 +165,28 @@ def q8_to_bf16(x, out: torch.Tensor):
     from . import launches
     launches.add()
     kernels().q8_to_bf16(x.q, x.d, out)
+
+
+class QWideLinear:
+    """GGUF dense projections of a wide forward on the tensor cores: the QWeight is decoded into a
+    bf16 copy (one reused buffer per shape) and multiplied with the bf16-weight tcgen05 GEMM."""
+
+    def __init__(self, device, status: torch.Tensor):
+        self.dev, self.status = device, status
+        self._buf: Dict[tuple, torch.Tensor] = {}
+
+    @staticmethod
+    def supports(w, rows_ok: bool = True) -> bool:
+        return w.fmt in GGUF_DEQUANT and w.K % 256 == 0
+
+    def linear(self, w, xb: torch.Tensor, y: torch.Tensor, residual: bool = False):
+        """y (+)= W xb for the rows of xb (y fp32 [rows, N], any row stride)."""
+        buf = self._buf.get((w.N, w.K))
+        if buf is None:
+            buf = self._buf[(w.N, w.K)] = torch.empty(w.N, w.K, dtype=torch.bfloat16, device=self.dev)
+        K = kernels()
+        K.qweight_dequant_bf16(w.fmt, w.planes, w.K, w.N, w.N, 0, buf)
+        rows = xb.shape[0]
+        K.tc_gemm_bf16(buf, xb, w.N, rows, y=y, atomic=residual, bn=128 if rows > 64 else 64, status=self.status)
+        from . import launches
+        launches.add(2)

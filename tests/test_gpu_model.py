@@ -117,13 +117,17 @@ def test_tiny_mixtral_logits_match_cpu_oracle(tiny_moe_gguf, native):
     cfg = config_from_gguf(m).with_(max_ctx=256)
     assert cfg.is_moe and cfg.n_experts == 4
     w = load_llama_weights(m, cfg, "cuda")
-    prompt = random_prompt(24, cfg.vocab, seed=2)
+    # 40 rows in one forward: experts as grouped tensor-core GEMMs and the Q8_0 projections as
+    # GEMMs over bf16 copies (the wide prefill path), against the C++ oracle
+    prompt = random_prompt(40, cfg.vocab, seed=2)
     cpu = native.CpuLlama(tiny_moe_gguf, 64, 8, True, True)
     ref = np.stack([cpu.forward(t, i) for i, t in enumerate(prompt)])
     eng = Engine.build(cfg, w, device="cuda", max_batch=2, max_ctx=256, block_size=16, num_blocks=64, max_rows=8)
     got = eng.model.forward_tokens(prompt, seq_id=3).cpu().numpy()
-    err = np.abs(got - ref).max()
-    assert err < 3e-2 * np.abs(ref).max(), err
+    # per position: a top-2 expert choice at a near tie can go either way between two correct
+    # forwards whose activations round differently, so 90 % of the positions must match closely
+    err = np.abs(got - ref).max(1) / np.abs(ref).max()
+    assert (err < 3e-2).mean() >= 0.9, err
     out = eng.generate([prompt], SamplingParams(max_tokens=6))[0]
     assert len(out) == 6
 
