@@ -184,7 +184,7 @@ def bench_qwen_next(args, sub: bool = False):
     max_blocks = -(-cfg.max_ctx // bs)
     kv = PagedKVCache(n_full, mcfg.n_kv_heads, cfg.head_dim, max_seqs * max_blocks + 8, bs, max_seqs, max_blocks, dev,
                       prefix_cache=False)
-    m = QwenNextModel(mcfg, w, kv, max_rows=512 if tp is None else 8, max_seqs=max_seqs, device=dev, tp=tp)
+    m = QwenNextModel(mcfg, w, kv, max_rows=2048, max_seqs=max_seqs, device=dev, tp=tp)
     g = torch.Generator(device=dev).manual_seed(1 + rank)
     for l in range(n_full):
         kv.k[l].normal_(0, 1, generator=g)
@@ -336,7 +336,7 @@ def bench_deepseek(args, sub: bool = False):
     bs, max_seqs = 64, 8
     max_blocks = -(-cfg.max_ctx // bs)
     kv = LatentCache(cfg.layers, max_seqs * max_blocks + 8, bs, max_seqs, max_blocks, dev)
-    m = DeepSeekModel(mcfg, w, kv, max_rows=512 if tp is None else 8, device=dev, tp=tp)
+    m = DeepSeekModel(mcfg, w, kv, max_rows=2048, device=dev, tp=tp)
     g = torch.Generator(device=dev).manual_seed(1)
     for lat in kv.latent:
         lat.normal_(0, 1, generator=g)

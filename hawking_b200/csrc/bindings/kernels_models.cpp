@@ -185,10 +185,10 @@ void tc_gemm_bf16(const Tensor& w, const Tensor& x, int64_t N, int64_t M, const 
 }
 
 void moe_tiles(const Tensor& counts, const Tensor& offsets, int64_t E1, int64_t bn, const Tensor& tiles,
-               const Tensor& n_tiles, bool pdl) {
+               const Tensor& n_tiles, bool pdl, int64_t e_lo, int64_t e_hi, int64_t shared_e) {
   const c10::cuda::CUDAGuard g(counts.device());
   hk::moe_tiles_launch(counts.data_ptr<int>(), offsets.data_ptr<int>(), (int)E1, (int)bn, tiles.data_ptr<int>(),
-                       n_tiles.data_ptr<int>(), cur_stream(), pdl);
+                       n_tiles.data_ptr<int>(), (int)e_lo, (int)e_hi, (int)shared_e, cur_stream(), pdl);
 }
 
 void moe_gather_bf16(const Tensor& sorted, int64_t PS, int64_t P, int64_t k, const Tensor& x, const Tensor& xg,
@@ -200,13 +200,15 @@ void moe_gather_bf16(const Tensor& sorted, int64_t PS, int64_t P, int64_t k, con
 }
 
 void moe_combine(const Tensor& y, const Tensor& pos, const Tensor& w, int64_t T, int64_t k, bool shared,
-                 const optional<Tensor>& shared_gate, const Tensor& x, bool pdl) {
+                 const optional<Tensor>& shared_gate, const Tensor& x, bool pdl, const optional<Tensor>& ids,
+                 int64_t e_lo, int64_t e_hi) {
   TORCH_CHECK(y.scalar_type() == at::kFloat && x.scalar_type() == at::kFloat, "moe_combine: fp32 rows");
   const c10::cuda::CUDAGuard g(x.device());
   hk::moe_combine_launch(y.data_ptr<float>(), y.stride(0), pos.data_ptr<int>(), w.data_ptr<float>(), (int)T, (int)k,
                          shared, shared_gate.has_value() ? shared_gate->data_ptr<float>() : nullptr,
                          shared_gate.has_value() ? (shared_gate->dim() > 1 ? shared_gate->stride(0) : 1) : 0,
-                         x.data_ptr<float>(), x.stride(0), (int)x.size(1), cur_stream(), pdl);
+                         x.data_ptr<float>(), x.stride(0), (int)x.size(1),
+                         ids.has_value() ? ids->data_ptr<int>() : nullptr, (int)e_lo, (int)e_hi, cur_stream(), pdl);
 }
 
 void qweight_dequant_bf16(int64_t fmt, const std::vector<Tensor>& planes, int64_t K, int64_t group_rows,
@@ -522,11 +524,13 @@ void register_model_kernels(py::module_& m) {
         py::arg("tiles") = py::none(), py::arg("n_tiles") = py::none(), py::arg("max_tiles") = 0,
         py::arg("group_rows") = 0);
   m.def("moe_tiles", &moe_tiles, py::arg("counts"), py::arg("offsets"), py::arg("E1"), py::arg("bn"),
-        py::arg("tiles"), py::arg("n_tiles"), py::arg("pdl") = false);
+        py::arg("tiles"), py::arg("n_tiles"), py::arg("pdl") = false, py::arg("e_lo") = 0, py::arg("e_hi") = 0,
+        py::arg("shared_e") = -1);
   m.def("moe_gather_bf16", &moe_gather_bf16, py::arg("sorted"), py::arg("PS"), py::arg("P"), py::arg("k"),
         py::arg("x"), py::arg("xg"), py::arg("pos"), py::arg("pdl") = false);
   m.def("moe_combine", &moe_combine, py::arg("y"), py::arg("pos"), py::arg("w"), py::arg("T"), py::arg("k"),
-        py::arg("shared"), py::arg("shared_gate"), py::arg("x"), py::arg("pdl") = false);
+        py::arg("shared"), py::arg("shared_gate"), py::arg("x"), py::arg("pdl") = false, py::arg("ids") = py::none(),
+        py::arg("e_lo") = 0, py::arg("e_hi") = 0);
   m.def("qweight_dequant_bf16", &qweight_dequant_bf16, py::arg("fmt"), py::arg("planes"), py::arg("K"),
         py::arg("group_rows"), py::arg("dst_group_rows"), py::arg("dst_off"), py::arg("out"), py::arg("pdl") = false);
   m.def("q8_to_bf16", &q8_to_bf16, py::arg("q"), py::arg("d"), py::arg("out"), py::arg("pdl") = false);

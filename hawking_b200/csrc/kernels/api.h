@@ -559,13 +559,13 @@ void mixed_gemv_launch(int epi, const MixedGemvArgs& a, cudaStream_t s, bool pdl
 // ---- prefill of the mixed-codec MoE models (moe_prefill.cu) ----
 void mixed_dequant_bf16_launch(const MixedDesc* desc, const int* didx, const int* drow, int count, int rows, int K,
                                __nv_bfloat16* out, int64_t out_stride, cudaStream_t s, bool pdl);
-void moe_tiles_launch(const int* counts, const int* offsets, int E1, int bn, int* tiles, int* n_tiles,
-                      cudaStream_t s, bool pdl);
+void moe_tiles_launch(const int* counts, const int* offsets, int E1, int bn, int* tiles, int* n_tiles, int e_lo,
+                      int e_hi, int shared_e, cudaStream_t s, bool pdl);
 void moe_gather_bf16_launch(const int* sorted, int PS, int P, int k, const __nv_bfloat16* x, int64_t x_stride, int K,
                             __nv_bfloat16* xg, int64_t xg_stride, int* pos, cudaStream_t s, bool pdl);
 void moe_combine_launch(const float* y, int64_t y_stride, const int* pos, const float* w, int T, int k, bool shared,
                         const float* shared_gate, int64_t gate_stride, float* x, int64_t x_stride, int H,
-                        cudaStream_t s, bool pdl);
+                        const int* ids, int e_lo, int e_hi, cudaStream_t s, bool pdl);
 void qweight_dequant_bf16_launch(int fmt, const WPlanes& w, int rows, int K, int group_rows, int dst_group_rows,
                                  int dst_off, __nv_bfloat16* out, int64_t out_stride, cudaStream_t s, bool pdl);
 void q8_to_bf16_launch(const int8_t* q, const float* d, int64_t q_stride, int64_t d_stride, int rows, int K,

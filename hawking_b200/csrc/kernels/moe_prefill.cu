@@ -185,12 +185,16 @@ void qweight_dequant_bf16_launch(int fmt, const WPlanes& w, int rows, int K, int
 }
 
 // Tiles of bn pairs per expert from the counting sort (one CTA; E1 <= 1024).
+// Under expert parallelism only this rank's experts [e_lo, e_hi) (e_hi = 0: all) and the folded
+// shared expert (shared_e, -1: none) get tiles.
 __global__ void __launch_bounds__(1024) moe_tiles_kernel(const int* counts, const int* offsets, int E1, int bn,
-                                                         int* tiles, int* n_tiles) {
+                                                         int* tiles, int* n_tiles, int e_lo, int e_hi,
+                                                         int shared_e) {
   __shared__ int pre[1025];
   pdl_wait();
   const int e = threadIdx.x;
-  const int c = e < E1 ? counts[e] : 0;
+  const bool mine = e_hi == 0 || (e >= e_lo && e < e_hi) || e == shared_e;
+  const int c = (e < E1 && mine) ? counts[e] : 0;
   const int nt = (c + bn - 1) / bn;
   pre[e + 1] = nt;
   if (e == 0) pre[0] = 0;
@@ -214,10 +218,11 @@ __global__ void __launch_bounds__(1024) moe_tiles_kernel(const int* counts, cons
   pdl_launch();
 }
 
-void moe_tiles_launch(const int* counts, const int* offsets, int E1, int bn, int* tiles, int* n_tiles,
-                      cudaStream_t s, bool pdl) {
+void moe_tiles_launch(const int* counts, const int* offsets, int E1, int bn, int* tiles, int* n_tiles, int e_lo,
+                      int e_hi, int shared_e, cudaStream_t s, bool pdl) {
   if (E1 > 1024) throw std::runtime_error("moe tiles: at most 1024 experts");
-  launch(moe_tiles_kernel, dim3(1), dim3(1024), 0, s, pdl, counts, offsets, E1, bn, tiles, n_tiles);
+  launch(moe_tiles_kernel, dim3(1), dim3(1024), 0, s, pdl, counts, offsets, E1, bn, tiles, n_tiles, e_lo, e_hi,
+         shared_e);
 }
 
 // Pair rows in sorted order (pairs below P are routed: token pair / k; the rest shared: pair - P),
@@ -245,16 +250,25 @@ void moe_gather_bf16_launch(const int* sorted, int PS, int P, int k, const __nv_
 
 // x[t] += sum_j w[t k + j] y[pos[t k + j]] (+ g(t) y[pos[P + t]] with a shared expert: g = 1, or
 // sigmoid of the shared-gate logit).
+// Under expert parallelism (ids given, e_hi > 0) only the pairs of this rank's experts [e_lo, e_hi)
+// were computed; the others are skipped.
 __global__ void __launch_bounds__(256) moe_combine_kernel(const float* y, int64_t y_stride, const int* pos,
                                                           const float* w, int T, int k, int shared,
                                                           const float* shared_gate, int64_t gate_stride, float* x,
-                                                          int64_t x_stride, int H) {
+                                                          int64_t x_stride, int H, const int* ids, int e_lo,
+                                                          int e_hi) {
   pdl_wait();
   const int t = blockIdx.y;
   const int n = blockIdx.x * blockDim.x + threadIdx.x;
   if (n < H) {
     float acc = 0.f;
-    for (int j = 0; j < k; ++j) acc += w[t * k + j] * y[(int64_t)pos[t * k + j] * y_stride + n];
+    for (int j = 0; j < k; ++j) {
+      if (ids && e_hi > 0) {
+        const int e = ids[t * k + j];
+        if (e < e_lo || e >= e_hi) continue;
+      }
+      acc += w[t * k + j] * y[(int64_t)pos[t * k + j] * y_stride + n];
+    }
     if (shared) {
       const float g = shared_gate ? 1.f / (1.f + __expf(-shared_gate[(int64_t)t * gate_stride])) : 1.f;
       acc += g * y[(int64_t)pos[T * k + t] * y_stride + n];
@@ -266,10 +280,10 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(const float* y, int64_
 
 void moe_combine_launch(const float* y, int64_t y_stride, const int* pos, const float* w, int T, int k, bool shared,
                         const float* shared_gate, int64_t gate_stride, float* x, int64_t x_stride, int H,
-                        cudaStream_t s, bool pdl) {
+                        const int* ids, int e_lo, int e_hi, cudaStream_t s, bool pdl) {
   if (T <= 0) return;
   launch(moe_combine_kernel, dim3((H + 255) / 256, T), dim3(256), 0, s, pdl, y, y_stride, pos, w, T, k,
-         shared ? 1 : 0, shared_gate, gate_stride, x, x_stride, H);
+         shared ? 1 : 0, shared_gate, gate_stride, x, x_stride, H, ids, e_lo, e_hi);
 }
 
 // int8 activation blocks (q, d per 32) -> bf16 rows.

@@ -130,8 +130,7 @@ class Engine:
                        block_size: int = 64, num_blocks: Optional[int] = None, kv_fraction: float = 0.5,
                        policy: int = 0, tp=None, prefill_rows: int = 2048):
         """Engine around the MLA + MoE model (paged latent cache; decode forwards of <= 8 rows;
-        prompts prefill in forwards of up to ``prefill_rows`` rows on one GPU, 8 under tensor
-        parallelism)."""
+        prompts prefill in forwards of up to ``prefill_rows`` rows)."""
         from ..models.deepseek import LAT, ROPE, DeepSeekModel, LatentCache
         max_ctx = max_ctx or cfg.max_ctx
         max_blocks = -(-max_ctx // block_size)
@@ -140,7 +139,7 @@ class Engine:
             bpb = cfg.layers * block_size * (LAT + ROPE) * 2
             num_blocks = min(int(free * kv_fraction // bpb), (max_batch + 1) * max_blocks + 16)
         kv = LatentCache(cfg.layers, num_blocks, block_size, max_batch + 1, max_blocks, device)
-        model = DeepSeekModel(cfg, weights, kv, max_rows=prefill_rows if tp is None else 8, device=device, tp=tp)
+        model = DeepSeekModel(cfg, weights, kv, max_rows=prefill_rows, device=device, tp=tp)
         return Engine(cfg, model, kv, max_batch=max_batch, max_prefill_tokens=model.row_limit, policy=policy)
 
     @staticmethod
@@ -162,9 +161,8 @@ class Engine:
             num_blocks = min(int(free * kv_fraction // bpb), (max_batch + 1) * max_blocks + 16)
         kv = PagedKVCache(max(1, n_full), cfg.n_kv_heads, cfg.head_dim, num_blocks, block_size, max_batch + 1,
                           max_blocks, device, prefix_cache=False)
-        # prompts prefill in forwards of up to prefill_rows rows on one GPU (8 under tensor parallelism)
-        model = QwenNextModel(cfg, weights, kv, max_rows=prefill_rows if tp is None else 8, max_seqs=max_batch + 1,
-                              device=device, tp=tp)
+        # prompts prefill in forwards of up to prefill_rows rows (decode forwards take up to 8)
+        model = QwenNextModel(cfg, weights, kv, max_rows=prefill_rows, max_seqs=max_batch + 1, device=device, tp=tp)
         return Engine(cfg, model, kv, max_batch=max_batch, max_prefill_tokens=max(model.row_limit, 8 * max_batch),
                       policy=policy)
 

@@ -150,7 +150,7 @@ class DeepSeekModel:
         # (the latent cache makes multi-row prefill exact; the absorb / output kernels run in
         # 8-row slices, the experts' kernels read each expert's weights once per CTA for all of its
         # pairs); tensor-parallel forwards stay at 8 rows (push all-reduce sites)
-        self.max_rows = R = max_rows if tp is None else min(max_rows, 8)
+        self.max_rows = R = max_rows
         self.max_logit_rows = min(R, 64)  # rows whose logits one forward can return
         dev = self.dev
         H, nh = cfg.hidden, cfg.n_heads
@@ -197,7 +197,7 @@ class DeepSeekModel:
         self.prefill = None  # ops/prefill.py MoePrefill, made at the first forward of more than 8 rows
         self.wide = None     # ops/prefill.py WideLinear (dense projections of wide forwards)
         self.xb = self.qab = self.attb = self.hb = None
-        if tp is None and R > 8:  # bf16 rows of the wide forwards' tensor-core GEMMs
+        if R > 8:  # bf16 rows of the wide forwards' tensor-core GEMMs
             bf = dict(dtype=torch.bfloat16, device=dev)
             self.xb = torch.zeros(R, H, **bf)
             self.qab = torch.zeros(R, max(cfg.q_lora_rank, 32), **bf)
@@ -205,6 +205,8 @@ class DeepSeekModel:
             self.hb = torch.zeros(R, max(cfg.ffn, 32), **bf)
         if tp is not None:
             self.x2 = torch.zeros(R, H, device=dev)  # second residual buffer of the push all-reduce
+            if R > 8:
+                self.partial = torch.zeros(R, H, device=dev)  # wide forwards: NCCL all-reduce partials
             self.argmax_slots = torch.zeros(R, ops.ARGMAX_SLOTS, dtype=torch.int64, device=dev)
         self._graphs = {}
         self.launches_per_graph = 0
@@ -223,7 +225,7 @@ class DeepSeekModel:
 
     def _wide(self, rows) -> bool:
         """This forward's projections run as tensor-core GEMMs over bf16 rows (prefill)."""
-        if self.tp is not None or rows <= 8 or self.xb is None:
+        if rows <= 8 or self.xb is None:
             return False
         c = self.cfg
         if any(d % 128 for d in (c.hidden, c.q_lora_rank, c.n_heads * c.v_head_dim)):
@@ -233,7 +235,9 @@ class DeepSeekModel:
             self.wide = WideLinear(self.w.table, self.dev, self.status)
         return True
 
-    def _attention(self, l, L, rows):
+    def _attention(self, l, L, rows, resid: Optional[torch.Tensor] = None):
+        """One layer's attention; the output projection adds to ``resid`` (default: the residual
+        rows; a zeroed partial under tensor parallelism for wide forwards)."""
         cfg, t, kv, inp = self.cfg, self.w.table, self.kv, self.inp
         K = kernels()
         xa = self.xa.view(rows)
@@ -296,7 +300,8 @@ class DeepSeekModel:
             nh, vd = cfg.n_heads, cfg.v_head_dim
             o = torch.bmm(self.o_lat[:rows].transpose(0, 1).to(torch.bfloat16), L.w_uv.transpose(1, 2))
             self.attb[:rows].view(rows, nh, vd).copy_(o.transpose(0, 1))
-            self.wide.linear(L.idx["o"], self.attb[:rows], self.x[:rows], residual=True)
+            self.wide.linear(L.idx["o"], self.attb[:rows], resid if resid is not None else self.x[:rows],
+                             residual=True)
             return
         for c0 in range(0, rows, 8):
             c1 = min(rows, c0 + 8)
@@ -306,7 +311,7 @@ class DeepSeekModel:
         else:
             mixed_gemv(t, L.idx["o"], self.attq.view(rows), self.x[:rows], residual=True)
 
-    def _ffn(self, L, rows, site: int = -1):
+    def _ffn(self, L, rows, site: int = -1, resid: Optional[torch.Tensor] = None):
         """FFN / MoE of one layer; under tensor parallelism (``site`` >= 0) the result is pushed to
         every rank's receive region of ``site`` instead of added to the residual."""
         cfg, t, tp = self.cfg, self.w.table, self.tp
@@ -314,7 +319,8 @@ class DeepSeekModel:
         if L.dense and self._wide(rows) and cfg.ffn % 64 == 0:
             ops.rmsnorm(self.x[:rows], L.ffn_norm, cfg.eps, yb=self.xb[:rows])
             self.wide.swiglu(L.idx["g"], L.idx["u"], self.xb[:rows], self.hb[:rows, :cfg.ffn])
-            self.wide.linear(L.idx["d"], self.hb[:rows, :cfg.ffn], self.x[:rows], residual=True)
+            self.wide.linear(L.idx["d"], self.hb[:rows, :cfg.ffn], resid if resid is not None else self.x[:rows],
+                             residual=True)
             return
         if L.dense:
             h = self.h.view(rows)
@@ -327,8 +333,8 @@ class DeepSeekModel:
         E, k, H, F = cfg.n_experts, cfg.top_k, cfg.hidden, cfg.expert_ffn
         ne = self.w.e_count or E  # routed experts in this rank's table
         e_lo = self.w.e_lo
-        if tp is None and rows > 8 and F % 128 == 0 and H % 128 == 0:
-            self._ffn_wide(L, rows)
+        if rows > 8 and F % 128 == 0 and H % 128 == 0:
+            self._ffn_wide(L, rows, resid if resid is not None else self.x[:rows])
             return
         fold = self.fold_shared and L.shared_here and L.idx.get("sg") == L.idx["eg"] + ne and \
             L.idx.get("su") == L.idx["eu"] + ne and L.idx.get("sd") == L.idx["ed"] + ne
@@ -375,7 +381,7 @@ class DeepSeekModel:
             mixed_gemv_swiglu(t, L.idx["sg"], L.idx["su"], xa, hs)
             mixed_gemv(t, L.idx["sd"], hs, self.x[:rows], residual=True)
 
-    def _ffn_wide(self, L, rows):
+    def _ffn_wide(self, L, rows, out: torch.Tensor):
         """Routed experts of a prefill forward on the tensor cores (ops/prefill.py): routing over
         the q8 rows, experts as two grouped GEMMs over the bf16 normed rows, deterministic
         combine; the shared expert folded in as one more group when it has the experts' width."""
@@ -391,19 +397,65 @@ class DeepSeekModel:
         ops.moe_topk(self.rlog[:rows], L.router_bias, k, self.scoring, cfg.n_groups, cfg.topk_groups, cfg.norm_topk,
                      cfg.routed_scale, self.ids[:rows], self.rw[:rows])
         ops.moe_align(self.ids[:rows], E, xa, self.counts, self.offsets, self.sorted, None, shared=fold)
-        self.prefill.run(L.idx, rows, k, self.xb[:rows], self.x[:rows], self.counts, self.offsets, self.sorted,
-                         self.rw[:rows], fold, pdl=ops.PDL)
+        # under expert parallelism this rank's experts only (the shared expert where it lives)
+        self.prefill.run(L.idx, rows, k, self.xb[:rows], out, self.counts, self.offsets, self.sorted,
+                         self.rw[:rows], fold, pdl=ops.PDL, e_lo=self.w.e_lo, e_count=self.w.e_count,
+                         ids=self.ids[:rows])
         if not fold and "sg" in L.idx:
-            self.prefill.dense_shared(L.idx, cfg.shared_ffn, rows, self.xb, self.x, pdl=ops.PDL)
+            self.prefill.dense_shared(L.idx, cfg.shared_ffn, rows, self.xb, out, pdl=ops.PDL)
 
     def forward(self, rows: int, sample: str = "greedy", advance: bool = False, n_logits: int = 0):
         """``n_logits`` (engine): > 0 moves the logits / greedy ids of ``logit_rows[:n_logits]`` to
         the first rows (all rows are computed; at most 8)."""
-        if self.tp is not None:
+        if self.tp is not None and rows > 8:
+            self._forward_tp_wide(rows, sample, advance, n_logits)
+        elif self.tp is not None:
             self._forward_tp(rows, sample, advance)
             compact_logit_rows(self, n_logits)
         else:
             self._forward_local(rows, sample, advance, n_logits)
+
+    def _forward_tp_wide(self, rows: int, sample: str, advance: bool, n_logits: int):
+        """Tensor / expert-parallel prefill forward of more than 8 rows: this rank's heads, dense
+        FFN slice and experts as tensor-core GEMMs into a zeroed partial, summed over the ranks by
+        an NCCL all-reduce after the attention and after the FFN (the push sites hold 8 rows); the
+        LM head runs on the sampled rows only (vocabulary slices, keys reduced as in decode)."""
+        import torch.distributed as dist
+        cfg, w, inp, tp = self.cfg, self.w, self.inp, self.tp
+        nl = n_logits if n_logits > 0 else (0 if n_logits < 0 else rows)
+        if nl > self.max_logit_rows:
+            raise ValueError(f"forward: logits for {nl} rows requested, at most {self.max_logit_rows}")
+        ops.tp_begin(tp)
+        x, xa, p = self.x[:rows], self.xa.view(rows), self.partial[:rows]
+        ops.embed(w.embed, inp.ids[:rows], x)
+        for l, L in enumerate(w.layers):
+            ops.rmsnorm_q8(x, L.attn_norm, cfg.eps, xa)
+            p.zero_()
+            self._attention(l, L, rows, resid=p)
+            dist.all_reduce(p, group=tp.group)
+            x.add_(p)
+            ops.rmsnorm_q8(x, L.ffn_norm, cfg.eps, xa)
+            p.zero_()
+            self._ffn(L, rows, resid=p)
+            dist.all_reduce(p, group=tp.group)
+            x.add_(p)
+        if nl:
+            ops.rmsnorm_q8(x, w.out_norm, cfg.eps, xa)
+            xh = xa
+            if n_logits > 0:
+                idx = self.logit_rows[:nl].long()
+                for src, dst in ((self.xa.q, self.xh.q), (self.xa.d, self.xh.d), (self.xa.s, self.xh.s)):
+                    torch.index_select(src, 0, idx, out=dst[:nl])
+                xh = self.xh.view(nl)
+            head = w.table.weights[w.lm_head]
+            if sample == "greedy" and nl <= 8:
+                mixed_gemv(w.table, w.lm_head, xh, self.logits[:nl], argmax_slots=self.argmax_slots[:nl],
+                           argmax_offset=tp.rank * head.N)
+                ops.tp_argmax(tp, self.argmax_slots, nl, self.next_ids)
+            else:  # logits only (this rank's vocabulary slice)
+                mixed_gemv(w.table, w.lm_head, xh, self.logits[:nl])
+        if advance:
+            ops.advance(inp.ids, self.next_ids, inp.positions, inp.row_ctx, rows)
 
     def _forward_local(self, rows: int, sample: str = "greedy", advance: bool = False, n_logits: int = 0):
         cfg, w, inp = self.cfg, self.w, self.inp

@@ -173,7 +173,7 @@ class QwenNextModel:
         # decode takes up to 8 rows; a prompt prefills in forwards of up to max_rows rows (every
         # kernel loops its rows; the expert kernels read each expert's codes once per CTA for all
         # of its pairs); tensor-parallel forwards stay at 8 rows (push all-reduce sites)
-        self.max_rows = R = max_rows if tp is None else min(max_rows, 8)
+        self.max_rows = R = max_rows
         self.max_logit_rows = min(R, 64)  # rows whose logits one forward can return
         dev = self.dev
         H, nh, nkv, hd = cfg.hidden, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
@@ -224,7 +224,7 @@ class QwenNextModel:
         self.prefill = None  # ops/prefill.py MoePrefill, made at the first forward of more than 8 rows
         self.wide = None     # ops/prefill.py WideLinear (dense projections of wide forwards)
         self.xb = self.attb = self.doutb = None
-        if tp is None and R > 8:  # bf16 rows of the wide forwards' tensor-core GEMMs
+        if R > 8:  # bf16 rows of the wide forwards' tensor-core GEMMs
             bf = dict(dtype=torch.bfloat16, device=dev)
             self.xb = torch.zeros(R, H, **bf)
             self.attb = torch.zeros(R, nh * hd, **bf)
@@ -235,6 +235,8 @@ class QwenNextModel:
             if not self.fused_route:
                 raise ValueError("qwen3next tensor parallelism needs the fused routing kernel (hidden % 512 == 0)")
             self.x2 = torch.zeros(R, H, device=dev)  # second residual buffer of the push all-reduce
+            if R > 8:
+                self.partial = torch.zeros(R, H, device=dev)  # wide forwards: NCCL all-reduce partials
             self.argmax_slots = torch.zeros(R, ops.ARGMAX_SLOTS, dtype=torch.int64, device=dev)
         self.next_ids = torch.zeros(R, dtype=torch.int32, device=dev)
         self.rope = ops.rope_table(cfg.max_ctx, cfg.rope_dim, cfg.rope_theta, None, dev)
@@ -264,7 +266,7 @@ class QwenNextModel:
 
     def _wide(self, rows) -> bool:
         """This forward's projections run as tensor-core GEMMs over bf16 rows (prefill)."""
-        if self.tp is not None or rows <= 8 or self.xb is None:
+        if rows <= 8 or self.xb is None:
             return False
         c, dm = self.cfg, self.dm
         if any(d % 128 for d in (c.hidden, c.n_heads * c.head_dim, dm["vdim"])):
@@ -274,7 +276,7 @@ class QwenNextModel:
             self.wide = WideLinear(self.w.table, self.dev, self.status)
         return True
 
-    def _full(self, l, L, rows, site: int = -1):
+    def _full(self, l, L, rows, site: int = -1, resid: Optional[torch.Tensor] = None):
         cfg, w, kv, inp = self.cfg, self.w, self.kv, self.inp
         nh, nkv, hd = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
         t, xa = w.table, self.xa.view(rows)
@@ -307,11 +309,12 @@ class QwenNextModel:
         elif wide:
             from ..ops.prefill import q8_to_bf16
             q8_to_bf16(self.attq.view(rows), self.attb[:rows])
-            self.wide.linear(L.idx["o"], self.attb[:rows], self.x[:rows], residual=True)
+            self.wide.linear(L.idx["o"], self.attb[:rows], resid if resid is not None else self.x[:rows],
+                             residual=True)
         else:
             mixed_gemv(t, L.idx["o"], self.attq.view(rows), self.x[:rows], residual=True)
 
-    def _linear(self, l, L, rows, site: int = -1):
+    def _linear(self, l, L, rows, site: int = -1, resid: Optional[torch.Tensor] = None):
         cfg, t, dm, inp = self.cfg, self.w.table, self.dm, self.inp
         xa = self.xa.view(rows)
         li = self.lin_index[l]
@@ -336,7 +339,8 @@ class QwenNextModel:
         elif wide:
             from ..ops.prefill import q8_to_bf16
             q8_to_bf16(self.dout.view(rows), self.doutb[:rows])
-            self.wide.linear(L.idx["out"], self.doutb[:rows], self.x[:rows], residual=True)
+            self.wide.linear(L.idx["out"], self.doutb[:rows], resid if resid is not None else self.x[:rows],
+                             residual=True)
         else:
             mixed_gemv(t, L.idx["out"], self.dout.view(rows), self.x[:rows], residual=True)
 
@@ -365,7 +369,7 @@ class QwenNextModel:
                          self.rw[:rows].reshape(-1), ops.PDL, rows * k, T=rows, push_table=tp.push_recv[site],
                          push_epoch=tp.epoch, shared_gate=self.sglog[:rows], **ep)
 
-    def _moe(self, L, rows):
+    def _moe(self, L, rows, resid: Optional[torch.Tensor] = None):
         cfg, t = self.cfg, self.w.table
         E, k, H, F = cfg.n_experts, cfg.top_k, cfg.hidden, cfg.expert_ffn
         xa = self.xa.view(rows)
@@ -380,9 +384,13 @@ class QwenNextModel:
             ops.rmsnorm(self.x[:rows], L.post_norm, cfg.eps, yb=self.xb[:rows])
             ops.router_logits(L.router, xa, self.rlog[:rows])
             ops.moe_topk(self.rlog[:rows], None, k, 0, 1, 1, cfg.norm_topk, 1.0, self.ids[:rows], self.rw[:rows])
-            ops.moe_align(self.ids[:rows], E, xa, self.counts, self.offsets, self.sorted, None, shared=True)
-            self.prefill.run(L.idx, rows, k, self.xb[:rows], self.x[:rows], self.counts, self.offsets, self.sorted,
-                             self.rw[:rows], True, shared_gate=self.sglog[:rows], pdl=ops.PDL)
+            # under expert parallelism: this rank's experts, and the shared expert where it lives
+            fold = "sg" in L.idx
+            ops.moe_align(self.ids[:rows], E, xa, self.counts, self.offsets, self.sorted, None, shared=fold)
+            self.prefill.run(L.idx, rows, k, self.xb[:rows], resid if resid is not None else self.x[:rows],
+                             self.counts, self.offsets, self.sorted, self.rw[:rows], fold,
+                             shared_gate=self.sglog[:rows], pdl=ops.PDL, e_lo=self.w.e_lo, e_count=self.w.e_count,
+                             ids=self.ids[:rows])
             return
         fused = self.fused_route and rows <= 8
         if fused:  # router GEMV, top-k, sort by expert and active list in one launch
@@ -413,13 +421,58 @@ class QwenNextModel:
         """``n_logits`` (engine): > 0 moves the logits / greedy ids of ``logit_rows[:n_logits]`` to
         the first rows. Rows must belong to distinct sequences (``serial_rows``)."""
         from .deepseek import compact_logit_rows
-        if self.tp is not None:
-            if rows > 8:
-                raise RuntimeError("tensor-parallel qwen3next forwards take at most 8 rows")
+        if self.tp is not None and rows > 8:
+            self._forward_tp_wide(rows, sample, advance, n_logits)
+        elif self.tp is not None:
             self._forward_tp(rows, sample, advance)
             compact_logit_rows(self, n_logits)
         else:
             self._forward(rows, sample, advance, n_logits)
+
+    def _forward_tp_wide(self, rows: int, sample: str, advance: bool, n_logits: int):
+        """Tensor / expert-parallel prefill forward of more than 8 rows: this rank's heads and
+        experts as tensor-core GEMMs into a zeroed partial, summed over the ranks by an NCCL
+        all-reduce after each mixer and each MoE block (the push sites hold 8 rows); the LM head
+        runs on the sampled rows only."""
+        import torch.distributed as dist
+        cfg, w, inp, tp = self.cfg, self.w, self.inp, self.tp
+        nl = n_logits if n_logits > 0 else (0 if n_logits < 0 else rows)
+        if nl > self.max_logit_rows:
+            raise ValueError(f"forward: logits for {nl} rows requested, at most {self.max_logit_rows}")
+        ops.tp_begin(tp)
+        x, xa, p = self.x[:rows], self.xa.view(rows), self.partial[:rows]
+        ops.embed(w.embed, inp.ids[:rows], x)
+        for l, L in enumerate(w.layers):
+            ops.rmsnorm_q8(x, L.attn_norm, cfg.eps, xa)
+            p.zero_()
+            if L.full:
+                self._full(l, L, rows, resid=p)
+            else:
+                self._linear(l, L, rows, resid=p)
+            dist.all_reduce(p, group=tp.group)
+            x.add_(p)
+            ops.rmsnorm_q8(x, L.post_norm, cfg.eps, xa)
+            p.zero_()
+            self._moe(L, rows, resid=p)
+            dist.all_reduce(p, group=tp.group)
+            x.add_(p)
+        if nl:
+            ops.rmsnorm_q8(x, w.out_norm, cfg.eps, xa)
+            xh = xa
+            if n_logits > 0:
+                idx = self.logit_rows[:nl].long()
+                for src, dst in ((self.xa.q, self.xh.q), (self.xa.d, self.xh.d), (self.xa.s, self.xh.s)):
+                    torch.index_select(src, 0, idx, out=dst[:nl])
+                xh = self.xh.view(nl)
+            head = w.table.weights[w.lm_head]
+            if sample == "greedy" and nl <= 8:
+                mixed_gemv(w.table, w.lm_head, xh, self.logits[:nl], argmax_slots=self.argmax_slots[:nl],
+                           argmax_offset=tp.rank * head.N)
+                ops.tp_argmax(tp, self.argmax_slots, nl, self.next_ids)
+            else:  # logits only (this rank's vocabulary slice)
+                mixed_gemv(w.table, w.lm_head, xh, self.logits[:nl])
+        if advance:
+            ops.advance(inp.ids, self.next_ids, inp.positions, inp.row_ctx, rows)
 
     def _forward_tp(self, rows: int, sample: str, advance: bool):
         cfg, w, inp, tp = self.cfg, self.w, self.inp, self.tp

@@ -43,33 +43,41 @@ class MoePrefill:
         self._lists: Dict[tuple, tuple] = {}
         self.shared_w: Optional[tuple] = None
 
-    def _lists_for(self, idx: Dict[str, int], fold: bool):
-        key = (idx["eg"], idx["eu"], idx["ed"], idx.get("sg", -1), fold)
+    def _lists_for(self, idx: Dict[str, int], fold: bool, e_lo: int, ne: int):
+        key = (idx["eg"], idx["eu"], idx["ed"], idx.get("sg", -1), fold, e_lo, ne)
         if key not in self._lists:
             E, F, H = self.E, self.F, self.H
             gi, gr, di, dr = [], [], [], []
-            n = E + (1 if fold else 0)
-            for e in range(n):
-                g, u, d = (idx["eg"] + e, idx["eu"] + e, idx["ed"] + e) if e < E else (idx["sg"], idx["su"], idx["sd"])
+            # table entry j of a matrix is expert e_lo + j (this rank's experts); the shared expert
+            # goes to slot E
+            slots = [(e_lo + j, idx["eg"] + j, idx["eu"] + j, idx["ed"] + j) for j in range(ne)]
+            if fold:
+                slots.append((E, idx["sg"], idx["su"], idx["sd"]))
+            for e, g, u, d in slots:
                 gi += [g, u]
                 gr += [2 * F * e, 2 * F * e + F]
                 di.append(d)
                 dr.append(H * e)
             t = lambda v: torch.tensor(v, dtype=torch.int32, device=self.dev)  # noqa: E731
-            self._lists[key] = (t(gi), t(gr), t(di), t(dr), n)
+            self._lists[key] = (t(gi), t(gr), t(di), t(dr), E + (1 if fold else 0))
         return self._lists[key]
 
     def run(self, idx: Dict[str, int], rows: int, k: int, xb: torch.Tensor, x: torch.Tensor, counts, offsets,
-            sorted_pairs, route_w, fold: bool, shared_gate: Optional[torch.Tensor] = None, pdl: bool = False):
+            sorted_pairs, route_w, fold: bool, shared_gate: Optional[torch.Tensor] = None, pdl: bool = False,
+            e_lo: int = 0, e_count: int = 0, ids: Optional[torch.Tensor] = None):
         """Experts of one layer for ``rows`` tokens. ``xb``: bf16 normed rows [rows, H]; ``x``: the
         fp32 residual rows (updated); counts / offsets / sorted_pairs from the counting sort
-        (with the shared expert as expert E when ``fold``); route_w [rows, k]."""
+        (with the shared expert as expert E when ``fold``); route_w [rows, k]. Under expert
+        parallelism (``e_count`` > 0) the table holds experts e_lo .. e_lo + e_count - 1 only:
+        just their pairs run, and ``ids`` [rows, k] tells the combine which pairs those are."""
         K = kernels()
-        gi, gr, di, dr, n = self._lists_for(idx, fold)
+        ne = e_count or self.E
+        gi, gr, di, dr, n = self._lists_for(idx, fold, e_lo if e_count else 0, ne)
         F, H = self.F, self.H
         K.mixed_dequant_bf16(self.table.descs, gi, gr, F, H, self.w_gu, pdl)
         K.mixed_dequant_bf16(self.table.descs, di, dr, H, F, self.w_dn, pdl)
-        self._experts(n, rows, k, xb, x, counts, offsets, sorted_pairs, route_w, fold, shared_gate, pdl)
+        self._experts(n, rows, k, xb, x, counts, offsets, sorted_pairs, route_w, fold, shared_gate, pdl,
+                      e_lo if e_count else 0, (e_lo + e_count) if e_count else 0, ids)
 
     def run_gguf(self, w_gate, w_up, w_down, rows: int, k: int, xb: torch.Tensor, x: torch.Tensor, counts,
                  offsets, sorted_pairs, route_w, pdl: bool = False):
@@ -82,19 +90,21 @@ class MoePrefill:
         K.qweight_dequant_bf16(w_down.fmt, w_down.planes, F, H, H, 0, self.w_dn, pdl)
         self._experts(self.E, rows, k, xb, x, counts, offsets, sorted_pairs, route_w, False, None, pdl)
 
-    def _experts(self, n, rows, k, xb, x, counts, offsets, sorted_pairs, route_w, fold, shared_gate, pdl):
+    def _experts(self, n, rows, k, xb, x, counts, offsets, sorted_pairs, route_w, fold, shared_gate, pdl,
+                 e_lo: int = 0, e_hi: int = 0, ids: Optional[torch.Tensor] = None):
         K = kernels()
         F, H = self.F, self.H
         P = rows * k
         PS = P + (rows if fold else 0)
-        K.moe_tiles(counts, offsets, n, BN, self.tiles, self.n_tiles, pdl)
+        K.moe_tiles(counts, offsets, n, BN, self.tiles, self.n_tiles, pdl, e_lo, e_hi, self.E if fold else -1)
         K.moe_gather_bf16(sorted_pairs, PS, P, k, xb, self.xg, self.pos, pdl)
         mt = (PS + BN - 1) // BN + n
         K.tc_gemm_bf16(self.w_gu, self.xg[:PS], 2 * F, PS, h=self.h, bn=BN, status=self.status, pdl=pdl,
                        tiles=self.tiles, n_tiles=self.n_tiles, max_tiles=mt, group_rows=2 * F)
         K.tc_gemm_bf16(self.w_dn, self.h[:PS], H, PS, y=self.y, bn=BN, status=self.status, pdl=pdl,
                        tiles=self.tiles, n_tiles=self.n_tiles, max_tiles=mt, group_rows=H)
-        K.moe_combine(self.y, self.pos, route_w, rows, k, fold, shared_gate, x, pdl)
+        K.moe_combine(self.y, self.pos, route_w, rows, k, fold, shared_gate, x, pdl, ids if e_hi else None, e_lo,
+                      e_hi)
         from . import launches
         launches.add(7)
 
