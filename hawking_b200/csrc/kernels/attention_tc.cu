@@ -51,8 +51,10 @@ template <int NC> struct Cfg {
 constexpr int kStages = 4;                    // ring stages at most (one KV block each)
 // Stages a launch uses (TcArgs.stages): 4, or 2 with HK_ATTN_STAGES=2 for blocks of 32 / 64 tokens
 // (a smaller ring leaves shared memory for the neighbouring kernels of the decode chain to be
-// resident at their programmatic launch). Parity soundness with 2 stages: at 64 tokens per block
-// every consumer visits every block; at 32 a consumer's blocks step by 2, all in one stage.
+// resident at their programmatic launch); launches of more than one wave take 3 for blocks of 64
+// and 2 for blocks of 32. Parity soundness with 2 or 3 stages: at 64 tokens per block every
+// consumer visits every block; at 32 (2 stages only) a consumer's blocks step by 2, all in one
+// stage.
 // Blocks of 16 keep 4 stages (a consumer's blocks step by 4).
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -60,7 +62,8 @@ struct TcArgs {
   const float* q;          // [R, nh, HD] fp32 (roped)
   const __nv_bfloat16* k_base;  // caches as raw pointers (speculative L2 prefetch)
   const __nv_bfloat16* v_base;
-  int stages;              // ring stages used (2 or 4)
+  int stages;              // ring stages used (2, 3 or 4)
+  int64_t pf_bytes;        // L2 prefetch cap per CTA (the launch's share of an L2 budget)
   int64_t cache_rows;
   int table_rows;
   const int* block_tables;
@@ -112,14 +115,18 @@ __global__ void __launch_bounds__(Cfg<NC>::kThreads, 2)
     // Before the dependency wait: L2 prefetch of this split's K/V blocks. The context length and
     // block table may still be changing (read speculatively, clamped to valid indices); only the
     // block the kernel before this one appends to is certain to be new, and a wrong guess costs
-    // a prefetch, never a result.
+    // a prefetch, never a result. Each CTA prefetches at most its share of an L2 budget: a wide
+    // batch (64 rows x 8 KV heads x 2048 tokens = 512 MB per layer) would otherwise evict its own
+    // prefetched lines before the ring reads them and fetch every byte twice.
     const int seq = a.row_seq[r], cx = a.row_ctx[r];
     if (seq >= 0 && seq < a.table_rows && cx > 0) {
       const int* bt = a.block_tables + (int64_t)seq * a.max_blocks;
       const int nbc = min((cx + bs - 1) / bs, a.max_blocks);
       const int per = (nbc + S - 1) / S;
-      const int e = min(nbc, split * per + per);
       const uint32_t bytes = (uint32_t)bs * HD * 2;
+      const int64_t pfb = a.pf_bytes / (2 * (int64_t)bytes);
+      const int cap = pfb < per ? (int)pfb : per;
+      const int e = min(nbc, split * per + cap);
       for (int i = split * per; i < e; ++i) {
         const int blk = bt[i];
         if (blk < 0 || (int64_t)(blk + 1) * a.nkv * bs > a.cache_rows) continue;
@@ -403,10 +410,22 @@ void launch_hd_nc(const AttnDecodeArgs& a, int64_t cache_rows, cudaStream_t s, b
     const char* e = getenv("HK_ATTN_STAGES");
     return e && atoi(e) == 2 ? 2 : kStages;
   }();
-  // Many CTAs (wide decode batches): a 2-stage ring lets several CTAs share an SM, which matters
-  // more than ring depth once the launch has more than one wave; few CTAs keep 4 stages.
+  // Many CTAs (wide decode batches): the launch has more than one wave and 2 CTAs share an SM
+  // (162 registers per thread), so ring depth sets the bytes in flight per SM. Blocks of 64 tokens
+  // take 3 stages (2 x 105 KB fits an SM; every consumer visits every block, so a 3-stage parity
+  // wait stays sound), blocks of 32 keep 2. Measured at Llama-3-8B bs64 (64 rows x 8 KV heads x
+  // 2048 tokens): 3 stages 98.9 us, 2 stages 100.6 us; 128 registers for 3 CTAs per SM with 2
+  // stages measured 126.9 us.
   const bool many = (int64_t)a.num_splits * a.nkv * a.R > 148;
-  t.stages = a.block_size == 16 ? kStages : (many ? 2 : env_stages);
+  if (a.block_size == 16) t.stages = kStages;
+  else if (!many) t.stages = env_stages;
+  else t.stages = a.block_size == 64 ? 3 : 2;
+  // L2 prefetch budget of the whole launch (default 48 MB of the 126 MB L2), split evenly per CTA
+  static const int64_t pf_budget = [] {
+    const char* e = getenv("HK_ATTN_PREFETCH_MB");
+    return (int64_t)(e ? atoi(e) : 48) << 20;
+  }();
+  t.pf_bytes = pf_budget / ((int64_t)a.num_splits * a.nkv * a.R);
   const size_t smem = 1024 + (size_t)t.stages * 2 * a.block_size * HD * 2;
   auto kern = attn_decode_tc_kernel<HD, NC>;
   HK_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));

@@ -11,8 +11,9 @@
 //   warps 4-11  dequantisers: raw smem -> bf16 A tile in the canonical K-major SW128 layout
 //               (bf16x2 FMAs of 128+q nibbles against the sub-block scale/min); warps 4-7 then run
 //               the epilogue (tcgen05.ld 32x32b -> coalesced fp32 stores or atomics)
-// Pipelines: raw (depth 4, TMA -> dequant warps) and A/X (depth 2, dequant warps + TMA -> UMMA,
-// released by tcgen05.commit). All waits are bounded and report through the status word.
+// Pipelines: raw (depth 4, TMA -> dequant warps), A (depth 2-3, dequant warps -> UMMA) and X
+// (depth 2-4, TMA -> UMMA), A and X released by tcgen05.commit. All waits are bounded and report
+// through the status word.
 //
 // SwiGLU variant (SW): the weight is the fused [gate | up] matrix of an FFN; tile i's 128 rows are
 // gate rows [64 i, 64 i + 64) and the matching up rows [F + 64 i, ...) (two 64-row TMA boxes per
@@ -104,6 +105,28 @@ __device__ __forceinline__ uint2 dq4(uint32_t v, int hi, __nv_bfloat162 s2, __nv
   return r;
 }
 
+// Shared memory of the one-tile kernel: the activation tile has a ring of its own (DX stages,
+// released by the MMA's commit), so its TMA loads run DX stages ahead instead of waiting for the
+// A stage they used to share: at 64 tokens per tile every launch spent about 1.2 us per K stage
+// with the activation load (L2 latency) on the critical path of each stage. Rings are deeper
+// where shared memory allows (tiles of <= 64 tokens: 3 A stages, 4 activation stages).
+template <int BN>
+struct OLayout {
+  static constexpr int DR = BN >= 256 ? 2 : DR_MAX;
+  static constexpr int DA = BN <= 64 ? 3 : 2;
+  static constexpr int DX = BN <= 64 ? 4 : (BN == 128 ? 3 : 2);
+  static constexpr uint32_t X_ATOM = BN * 128;
+  static constexpr uint32_t X_STAGE = 2 * X_ATOM;
+  static constexpr uint32_t off_a = 0;
+  static constexpr uint32_t off_x = off_a + DA * A_STAGE;
+  static constexpr uint32_t off_hdr = off_x + DX * X_STAGE;
+  static constexpr uint32_t off_qs = off_hdr + DR * RAW_HDR;
+  static constexpr uint32_t off_bar = off_qs + DR * RAW_QS;
+  static constexpr uint32_t n_bars = 2 * DR + 2 * DA + 2 * DX + 1;
+  static constexpr uint32_t total = off_bar + n_bars * 8 + 16 + 1024;  // + alignment slack
+  static_assert(total <= 232448, "tc_gemm: shared memory over the 227 KB per-CTA limit");
+};
+
 // ABF: the weights are bf16 [rows, K] already (a dequantised copy): warp 0 loads them with TMA
 // straight into the A stages (tm_hdr is their map, tm_qs unused) and the dequantisers only run
 // the epilogue.
@@ -111,7 +134,8 @@ template <int BN, bool SW, bool ABF>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_q4k_kernel(const __grid_constant__ CUtensorMap tm_hdr, const __grid_constant__ CUtensorMap tm_qs,
                        const __grid_constant__ CUtensorMap tm_x, TcArgs a) {
-  using L = Layout<BN>;
+  using L = OLayout<BN>;
+  constexpr int DA = L::DA, DX = L::DX;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::off_bar);
@@ -119,7 +143,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* raw_empty = bars + L::DR;
   uint64_t* a_full = bars + 2 * L::DR;
   uint64_t* a_empty = bars + 2 * L::DR + DA;
-  uint64_t* acc_full = bars + 2 * L::DR + 2 * DA;
+  uint64_t* x_full = bars + 2 * L::DR + 2 * DA;
+  uint64_t* x_empty = x_full + DX;
+  uint64_t* acc_full = x_empty + DX;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::n_bars);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -141,7 +167,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < L::DR; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], kDequantWarps); }
-    for (int i = 0; i < DA; ++i) { mbar_init(&a_full[i], ABF ? 2 : kDequantWarps + 1); mbar_init(&a_empty[i], 1); }
+    for (int i = 0; i < DA; ++i) { mbar_init(&a_full[i], ABF ? 1 : kDequantWarps); mbar_init(&a_empty[i], 1); }
+    for (int i = 0; i < DX; ++i) { mbar_init(&x_full[i], 1); mbar_init(&x_empty[i], 1); }
     mbar_init(acc_full, 1);
     fence_barrier_init();
   }
@@ -203,13 +230,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---- activation producer ----
       int issued = 0;
       for (int i = 0; i < nst; ++i) {
-        const int slot = i % DA;
-        if (!mbar_wait(&a_empty[slot], ((i / DA) & 1) ^ 1, a.status)) break;
+        const int slot = i % DX;
+        if (!mbar_wait(&x_empty[slot], ((i / DX) & 1) ^ 1, a.status)) break;
         const int gs = s0 + i;
-        mbar_arrive_expect_tx(&a_full[slot], L::X_STAGE);
+        mbar_arrive_expect_tx(&x_full[slot], L::X_STAGE);
         uint8_t* xs = smem + L::off_x + slot * L::X_STAGE;
-        tma_load_2d(xs, &tm_x, gs * BK, m0, &a_full[slot]);
-        tma_load_2d(xs + L::X_ATOM, &tm_x, gs * BK + 64, m0, &a_full[slot]);
+        tma_load_2d(xs, &tm_x, gs * BK, m0, &x_full[slot]);
+        tma_load_2d(xs + L::X_ATOM, &tm_x, gs * BK + 64, m0, &x_full[slot]);
         ++issued;
       }
       if (issued < nst) {  // error path: give copies in flight time to land before exiting
@@ -220,12 +247,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
       bool ok = true;
       for (int i = 0; i < nst && ok; ++i) {
-        const int slot = i % DA;
-        ok = mbar_wait(&a_full[slot], (i / DA) & 1, a.status);
+        const int slot = i % DA, xslot = i % DX;
+        ok = mbar_wait(&a_full[slot], (i / DA) & 1, a.status) && mbar_wait(&x_full[xslot], (i / DX) & 1, a.status);
         if (!ok) break;
         tc_fence_after();
         const uint32_t a_base = smem_u32(smem + L::off_a + slot * A_STAGE);
-        const uint32_t x_base = smem_u32(smem + L::off_x + slot * L::X_STAGE);
+        const uint32_t x_base = smem_u32(smem + L::off_x + xslot * L::X_STAGE);
 #pragma unroll
         for (int c = 0; c < 2; ++c)
 #pragma unroll
@@ -235,6 +262,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             umma_f16(tmem, ad, bd, idesc, (i | c | kk) != 0);
           }
         umma_commit(&a_empty[slot]);
+        umma_commit(&x_empty[xslot]);
         if (a.serialize) ok = mbar_wait(&a_empty[slot], (i / DA) & 1, a.status);  // debug: no MMA/dequant overlap
       }
       umma_commit(acc_full);
@@ -876,7 +904,7 @@ CUtensorMap make_map_2d(CUtensorMapDataType dt, const void* base, uint64_t inner
 
 template <int BN, bool SW>
 void launch_bn(const TcGemmArgs& g, cudaStream_t s) {
-  using L = Layout<BN>;
+  using L = OLayout<BN>;
   const uint64_t rb = (uint64_t)g.w_row_bytes, hb = (uint64_t)g.w_hdr_row_bytes;
   const uint32_t box_rows = SW ? BM / 2 : BM;
   CUtensorMap tm_hdr = make_map_2d(CU_TENSOR_MAP_DATA_TYPE_UINT8, g.w_hdr, hb, g.N, hb, 16, box_rows,
@@ -1006,7 +1034,7 @@ void launch_pair(const TcGemmArgs& g, cudaStream_t s) {
 
 template <int BN, bool SW>
 void launch_abf(const TcBf16Args& g, cudaStream_t s) {
-  using L = Layout<BN>;
+  using L = OLayout<BN>;
   const uint32_t box_rows = SW ? BM / 2 : BM;
   CUtensorMap tm_a = make_map_2d(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, g.w, g.K, g.w_rows, (uint64_t)g.w_stride * 2, 64,
                                  box_rows, CU_TENSOR_MAP_SWIZZLE_128B);
