@@ -25,7 +25,7 @@ void quantize(int64_t fmt, const Tensor& x, const std::vector<Tensor>& planes) {
 }
 void tc_gemm(int64_t fmt, const std::vector<Tensor>& planes, int64_t N, int64_t K, const Tensor& x, const Tensor& y,
              bool atomic, bool y_zeroed, int64_t k_splits, int64_t bn, const Tensor& status, bool pdl,
-             const c10::optional<Tensor>& h, bool persistent) {
+             const c10::optional<Tensor>& h, bool persistent, bool stream_k) {
   TORCH_CHECK(planes.size() == 2, "tc_gemm: Q4_K expects [quants, headers] planes");
   const Tensor& w = planes[0];
   const Tensor& wh = planes[1];
@@ -53,7 +53,7 @@ void tc_gemm(int64_t fmt, const std::vector<Tensor>& planes, int64_t N, int64_t 
   g.bn = (int)bn;
   g.status = status.data_ptr<int>();
   g.pdl = pdl;
-  g.persistent = persistent ? 1 : 0;
+  g.persistent = stream_k ? 2 : (persistent ? 1 : 0);
   if (h.has_value()) {
     TORCH_CHECK(h->scalar_type() == at::kBFloat16 && h->stride(-1) == 1 && h->size(0) >= g.M && h->size(1) >= N / 2,
                 "tc_gemm swiglu: h must be bf16 [M, >= N / 2]");
@@ -236,7 +236,8 @@ void register_more_kernels(py::module_& m) {
   m.def("quantize", &quantize, py::arg("fmt"), py::arg("x"), py::arg("planes"));
   m.def("tc_gemm", &tc_gemm, py::arg("fmt"), py::arg("planes"), py::arg("N"), py::arg("K"), py::arg("x"), py::arg("y"),
         py::arg("atomic"), py::arg("y_zeroed"), py::arg("k_splits"), py::arg("bn"), py::arg("status"),
-        py::arg("pdl") = false, py::arg("h") = py::none(), py::arg("persistent") = false);
+        py::arg("pdl") = false, py::arg("h") = py::none(), py::arg("persistent") = false,
+        py::arg("stream_k") = false);
   m.def("tc_gemm_splits", &hk::tc_gemm_splits);
   m.def("router_logits", &router_logits, py::arg("w"), py::arg("xq"), py::arg("xd"), py::arg("logits"),
         py::arg("pdl") = false);

@@ -391,7 +391,8 @@ struct TcGemmArgs {
   __nv_bfloat16* h;
   int64_t h_stride;
   // persistent launch (one CTA per SM looping over tiles, epilogue overlapped with the next
-  // tile's main loop); no split-K
+  // tile's main loop); no split-K. 2: stream-K, every CTA one balanced range of (tile, K stage)
+  // units, partial tiles accumulated with atomics (atomic or zeroed y; no SwiGLU)
   int persistent;
 };
 int tc_gemm_splits(int N, int M, int K, int bn, int sms);

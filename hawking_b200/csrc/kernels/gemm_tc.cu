@@ -45,7 +45,6 @@ constexpr int BM = 128;        // weight rows per tile (UMMA M)
 constexpr int BK = 128;        // K per stage (half a Q4_K super-block)
 constexpr int DA = 2;          // A/X stages
 constexpr int DR_MAX = 4;      // raw weight stages (2 at BN = 256, where shared memory is short)
-constexpr int kThreads = 384;
 constexpr int kDequantWarp0 = 4;
 constexpr int kDequantWarps = 8;
 constexpr uint32_t A_ATOM = BM * 128;       // 16 KB: 128 rows x 64 bf16
@@ -85,6 +84,9 @@ struct TcArgs {
   const int* tiles;
   const int* n_tiles;
   int group_rows;
+  // persistent kernel, stream-K: CTA b takes the units [b U / G, (b + 1) U / G) of the
+  // U = tiles x K-stages units (tile major), accumulating partial tiles into y with atomics
+  int stream_k;
 };
 
 __device__ __forceinline__ uint32_t bf2_bits(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t*>(&v); }
@@ -115,6 +117,10 @@ struct OLayout {
   static constexpr int DR = BN >= 256 ? 2 : DR_MAX;
   static constexpr int DA = BN <= 64 ? 3 : 2;
   static constexpr int DX = BN <= 64 ? 4 : (BN == 128 ? 3 : 2);
+  // dequantising warps (half a weight row each); 16 warps with a quarter row each measured slower
+  // at 64 tokens per tile (gate/up 66.8 -> 71.1 us)
+  static constexpr int DQW = 8;
+  static constexpr int THREADS = (kDequantWarp0 + DQW) * 32;
   static constexpr uint32_t X_ATOM = BN * 128;
   static constexpr uint32_t X_STAGE = 2 * X_ATOM;
   static constexpr uint32_t off_a = 0;
@@ -131,11 +137,11 @@ struct OLayout {
 // straight into the A stages (tm_hdr is their map, tm_qs unused) and the dequantisers only run
 // the epilogue.
 template <int BN, bool SW, bool ABF>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(OLayout<BN>::THREADS, 1)
     tc_gemm_q4k_kernel(const __grid_constant__ CUtensorMap tm_hdr, const __grid_constant__ CUtensorMap tm_qs,
                        const __grid_constant__ CUtensorMap tm_x, TcArgs a) {
   using L = OLayout<BN>;
-  constexpr int DA = L::DA, DX = L::DX;
+  constexpr int DA = L::DA, DX = L::DX, DQW = L::DQW;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::off_bar);
@@ -166,8 +172,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t tmem_cols = BN < 32 ? 32 : BN;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < L::DR; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], kDequantWarps); }
-    for (int i = 0; i < DA; ++i) { mbar_init(&a_full[i], ABF ? 1 : kDequantWarps); mbar_init(&a_empty[i], 1); }
+    for (int i = 0; i < L::DR; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], DQW); }
+    for (int i = 0; i < DA; ++i) { mbar_init(&a_full[i], ABF ? 1 : DQW); mbar_init(&a_empty[i], 1); }
     for (int i = 0; i < DX; ++i) { mbar_init(&x_full[i], 1); mbar_init(&x_empty[i], 1); }
     mbar_init(acc_full, 1);
     fence_barrier_init();
@@ -266,17 +272,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (a.serialize) ok = mbar_wait(&a_empty[slot], (i / DA) & 1, a.status);  // debug: no MMA/dequant overlap
       }
       umma_commit(acc_full);
-    } else if (!ABF && warp >= kDequantWarp0 && warp < kDequantWarp0 + kDequantWarps) {
+    } else if (!ABF && warp >= kDequantWarp0 && warp < kDequantWarp0 + DQW) {
       // ---- dequantisers ----
+      // TPR threads per weight row: thread (r, c, p) expands quant bytes [32 c + 16 p, + 16 NQ) of
+      // the row's 64-byte chunk, i.e. the low nibbles into sub-block 2 c and the high nibbles into
+      // sub-block 2 c + 1 of the stage's half super-block
+      constexpr int TPR = DQW * 32 / BM;   // 2 or 4
+      constexpr int NQ = 4 / TPR;          // 16-byte quant pieces per thread: 2 or 1
       const int t = (warp - kDequantWarp0) * 32 + lane;
-      const int r = t >> 1, c = t & 1;
+      const int r = t / TPR, c = (t % TPR) / (TPR / 2), p = t % (TPR / 2);
       for (int i = 0; i < nst; ++i) {
         const int rs = i % L::DR, as = i % DA;
         const bool ok_raw = __shfl_sync(0xffffffffu, mbar_wait(&raw_full[rs], (i / L::DR) & 1, a.status), 0);
         if (!ok_raw) break;
         const uint4 hdr = *reinterpret_cast<const uint4*>(smem + L::off_hdr + rs * RAW_HDR + r * 16);
-        const uint4 q0 = *reinterpret_cast<const uint4*>(smem + L::off_qs + rs * RAW_QS + r * 64 + c * 32);
-        const uint4 q1 = *reinterpret_cast<const uint4*>(smem + L::off_qs + rs * RAW_QS + r * 64 + c * 32 + 16);
+        uint32_t w[4 * NQ];
+#pragma unroll
+        for (int e = 0; e < NQ; ++e) {
+          const uint4 qv = *reinterpret_cast<const uint4*>(smem + L::off_qs + rs * RAW_QS + r * 64 + c * 32 +
+                                                           (p * NQ + e) * 16);
+          w[4 * e] = qv.x;
+          w[4 * e + 1] = qv.y;
+          w[4 * e + 2] = qv.z;
+          w[4 * e + 3] = qv.w;
+        }
         const int gs = s0 + i, h = gs & 1;
         const int j0 = 4 * h + 2 * c;
         int sc0, mn0, sc1, mn1;
@@ -290,11 +309,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool ok_a = __shfl_sync(0xffffffffu, mbar_wait(&a_empty[as], ((i / DA) & 1) ^ 1, a.status), 0);
         if (!ok_a) break;
         uint8_t* atom = smem + L::off_a + as * A_STAGE + c * A_ATOM;
-        const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
-        for (int ch = 0; ch < 4; ++ch) {  // 16-byte chunk = 8 elements = 2 words
-          const uint2 lo0 = dq4(w[2 * ch], 0, s2A, o2A), lo1 = dq4(w[2 * ch + 1], 0, s2A, o2A);
-          const uint2 hi0 = dq4(w[2 * ch], 1, s2B, o2B), hi1 = dq4(w[2 * ch + 1], 1, s2B, o2B);
+        for (int cc = 0; cc < 2 * NQ; ++cc) {  // 16-byte chunk = 8 elements = 2 words
+          const int ch = p * 2 * NQ + cc;
+          const uint2 lo0 = dq4(w[2 * cc], 0, s2A, o2A), lo1 = dq4(w[2 * cc + 1], 0, s2A, o2A);
+          const uint2 hi0 = dq4(w[2 * cc], 1, s2B, o2B), hi1 = dq4(w[2 * cc + 1], 1, s2B, o2B);
           *reinterpret_cast<uint4*>(atom + sw128_offset(r, ch)) = make_uint4(lo0.x, lo0.y, lo1.x, lo1.y);
           *reinterpret_cast<uint4*>(atom + sw128_offset(r, ch + 4)) = make_uint4(hi0.x, hi0.y, hi1.x, hi1.y);
         }
@@ -396,10 +415,20 @@ constexpr int kPEpi0 = kDequantWarp0 + kPDequantWarps;
 
 template <int BN>
 struct PLayout {
-  using L = Layout<BN>;
-  static constexpr uint32_t off_park = L::off_bar;                  // SwiGLU exchange [2][64][8] fp32
+  // rings as in the one-tile kernel: A (dequantisers -> UMMA), X (TMA -> UMMA) and raw (TMA ->
+  // dequantisers), deeper where shared memory allows (tiles of 64 tokens: 3 A, 4 X stages)
+  static constexpr int DR = BN >= 256 ? 2 : DR_MAX;
+  static constexpr int DA = BN <= 64 ? 3 : 2;
+  static constexpr int DX = BN <= 64 ? 4 : 2;
+  static constexpr uint32_t X_ATOM = BN * 128;
+  static constexpr uint32_t X_STAGE = 2 * X_ATOM;
+  static constexpr uint32_t off_a = 0;
+  static constexpr uint32_t off_x = off_a + DA * A_STAGE;
+  static constexpr uint32_t off_hdr = off_x + DX * X_STAGE;
+  static constexpr uint32_t off_qs = off_hdr + DR * RAW_HDR;
+  static constexpr uint32_t off_park = off_qs + DR * RAW_QS;       // SwiGLU exchange [2][64][8] fp32
   static constexpr uint32_t off_bar = off_park + 2 * 64 * 8 * 4;
-  static constexpr uint32_t n_bars = 2 * L::DR + 2 * DA + 4;
+  static constexpr uint32_t n_bars = 2 * DR + 2 * DA + 2 * DX + 4;
   static constexpr uint32_t total = off_bar + n_bars * 8 + 16 + 1024;
   static_assert(total <= 232448, "tc_gemm persistent: shared memory over the 227 KB per-CTA limit");
 };
@@ -408,9 +437,9 @@ template <int BN, bool SW>
 __global__ void __launch_bounds__(kPThreads, 1)
     tc_gemm_q4k_persistent(const __grid_constant__ CUtensorMap tm_hdr, const __grid_constant__ CUtensorMap tm_qs,
                            const __grid_constant__ CUtensorMap tm_x, TcArgs a) {
-  using L = Layout<BN>;
   using P = PLayout<BN>;
-  constexpr int PDR = L::DR, PDA = DA;
+  using L = P;  // ring offsets
+  constexpr int PDR = P::DR, PDA = P::DA, PDX = P::DX;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P::off_bar);
@@ -418,7 +447,9 @@ __global__ void __launch_bounds__(kPThreads, 1)
   uint64_t* raw_empty = bars + PDR;
   uint64_t* a_full = bars + 2 * PDR;
   uint64_t* a_empty = bars + 2 * PDR + PDA;
-  uint64_t* acc_full = bars + 2 * PDR + 2 * PDA;   // [2]
+  uint64_t* x_full = bars + 2 * PDR + 2 * PDA;
+  uint64_t* x_empty = x_full + PDX;
+  uint64_t* acc_full = x_empty + PDX;              // [2]
   uint64_t* acc_empty = acc_full + 2;              // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + P::n_bars);
   float* park = reinterpret_cast<float*>(smem + P::off_park);
@@ -430,10 +461,42 @@ __global__ void __launch_bounds__(kPThreads, 1)
   const int tiles = m_tiles * n_tiles;
   const int nst = a.K / BK;
   constexpr uint32_t tmem_cols = 2 * BN;
+  // work list: tiles blockIdx.x, + gridDim.x, ... (whole K each), or under stream-K one balanced
+  // range of (tile, stage) units; segment j is a run of stages [ka, kb) of one tile t
+  const int64_t units = (int64_t)tiles * nst;
+  const int64_t u_lo = a.stream_k ? units * blockIdx.x / gridDim.x : 0;
+  const int64_t u_hi = a.stream_k ? units * (blockIdx.x + 1) / gridDim.x : 0;
+  auto first_seg = [&](int& t, int& ka, int& kb) {
+    if (a.stream_k) {
+      t = (int)(u_lo / nst);
+      ka = (int)(u_lo - (int64_t)t * nst);
+      kb = (int)(ka + (u_hi - u_lo) < nst ? ka + (u_hi - u_lo) : nst);
+      if (u_hi <= u_lo) t = tiles;
+    } else {
+      t = blockIdx.x;
+      ka = 0;
+      kb = nst;
+    }
+  };
+  auto next_seg = [&](int& t, int& ka, int& kb) {
+    if (a.stream_k) {
+      const int64_t u = (int64_t)t * nst + kb;  // first unit after this segment
+      if (u >= u_hi) {
+        t = tiles;
+        return;
+      }
+      t += 1;
+      ka = 0;
+      kb = (int)(u_hi - u < nst ? u_hi - u : nst);
+    } else {
+      t += gridDim.x;
+    }
+  };
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < PDR; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], kPDequantWarps); }
-    for (int i = 0; i < PDA; ++i) { mbar_init(&a_full[i], kPDequantWarps + 1); mbar_init(&a_empty[i], 1); }
+    for (int i = 0; i < PDA; ++i) { mbar_init(&a_full[i], kPDequantWarps); mbar_init(&a_empty[i], 1); }
+    for (int i = 0; i < PDX; ++i) { mbar_init(&x_full[i], 1); mbar_init(&x_empty[i], 1); }
     for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 4); }
     fence_barrier_init();
   }
@@ -449,23 +512,24 @@ __global__ void __launch_bounds__(kPThreads, 1)
     // ---- raw Q4_K producer: stage s = half (s & 1) of super-block (s >> 1) ----
     int it = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+    int t, ka, kb;
+    for (first_seg(t, ka, kb); t < tiles && ok; next_seg(t, ka, kb)) {
       const int n0 = (t / m_tiles) * RB;
-      for (int s = 0; s < nst; ++s, ++it) {
+      for (int s = ka; s < kb; ++s, ++it) {
         const int slot = it % PDR;
         if (!(ok = mbar_wait(&raw_empty[slot], ((it / PDR) & 1) ^ 1, a.status))) break;
-        const int sb = s >> 1, h = s & 1;
+        const int sbk = s >> 1, h = s & 1;
         mbar_arrive_expect_tx(&raw_full[slot], RAW_HDR + RAW_QS);
         uint8_t* hd = smem + L::off_hdr + slot * RAW_HDR;
         uint8_t* qd = smem + L::off_qs + slot * RAW_QS;
         if constexpr (SW) {
-          tma_load_2d(hd, &tm_hdr, sb * 16, n0, &raw_full[slot]);
-          tma_load_2d(hd + RAW_HDR / 2, &tm_hdr, sb * 16, a.F + n0, &raw_full[slot]);
-          tma_load_2d(qd, &tm_qs, (2 * sb + h) * 64, n0, &raw_full[slot]);
-          tma_load_2d(qd + RAW_QS / 2, &tm_qs, (2 * sb + h) * 64, a.F + n0, &raw_full[slot]);
+          tma_load_2d(hd, &tm_hdr, sbk * 16, n0, &raw_full[slot]);
+          tma_load_2d(hd + RAW_HDR / 2, &tm_hdr, sbk * 16, a.F + n0, &raw_full[slot]);
+          tma_load_2d(qd, &tm_qs, (2 * sbk + h) * 64, n0, &raw_full[slot]);
+          tma_load_2d(qd + RAW_QS / 2, &tm_qs, (2 * sbk + h) * 64, a.F + n0, &raw_full[slot]);
         } else {
-          tma_load_2d(hd, &tm_hdr, sb * 16, n0, &raw_full[slot]);
-          tma_load_2d(qd, &tm_qs, (2 * sb + h) * 64, n0, &raw_full[slot]);
+          tma_load_2d(hd, &tm_hdr, sbk * 16, n0, &raw_full[slot]);
+          tma_load_2d(qd, &tm_qs, (2 * sbk + h) * 64, n0, &raw_full[slot]);
         }
       }
     }
@@ -475,15 +539,16 @@ __global__ void __launch_bounds__(kPThreads, 1)
     // ---- activation producer ----
     int it = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+    int t, ka, kb;
+    for (first_seg(t, ka, kb); t < tiles && ok; next_seg(t, ka, kb)) {
       const int m0 = (t % m_tiles) * BN;
-      for (int s = 0; s < nst; ++s, ++it) {
-        const int slot = it % PDA;
-        if (!(ok = mbar_wait(&a_empty[slot], ((it / PDA) & 1) ^ 1, a.status))) break;
-        mbar_arrive_expect_tx(&a_full[slot], L::X_STAGE);
-        uint8_t* xs = smem + L::off_x + slot * L::X_STAGE;
-        tma_load_2d(xs, &tm_x, s * BK, m0, &a_full[slot]);
-        tma_load_2d(xs + L::X_ATOM, &tm_x, s * BK + 64, m0, &a_full[slot]);
+      for (int s = ka; s < kb; ++s, ++it) {
+        const int slot = it % PDX;
+        if (!(ok = mbar_wait(&x_empty[slot], ((it / PDX) & 1) ^ 1, a.status))) break;
+        mbar_arrive_expect_tx(&x_full[slot], P::X_STAGE);
+        uint8_t* xs = smem + P::off_x + slot * P::X_STAGE;
+        tma_load_2d(xs, &tm_x, s * BK, m0, &x_full[slot]);
+        tma_load_2d(xs + P::X_ATOM, &tm_x, s * BK + 64, m0, &x_full[slot]);
       }
     }
     if (!ok) for (int k = 0; k < 2000; ++k) __nanosleep(100);  // error path: let copies in flight land
@@ -492,24 +557,28 @@ __global__ void __launch_bounds__(kPThreads, 1)
     constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
     int it = 0, j = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++j) {
+    int t, ka, kb;
+    for (first_seg(t, ka, kb); t < tiles && ok; next_seg(t, ka, kb), ++j) {
       const int ab = j & 1;
       if (!(ok = mbar_wait(&acc_empty[ab], ((j >> 1) & 1) ^ 1, a.status))) break;
       tc_fence_after();
       const uint32_t acc = tmem + (uint32_t)(ab * BN);
-      for (int s = 0; s < nst; ++s, ++it) {
-        const int slot = it % PDA;
-        if (!(ok = mbar_wait(&a_full[slot], (it / PDA) & 1, a.status))) break;
+      for (int s = ka; s < kb; ++s, ++it) {
+        const int slot = it % PDA, xslot = it % PDX;
+        if (!(ok = mbar_wait(&a_full[slot], (it / PDA) & 1, a.status) &&
+                   mbar_wait(&x_full[xslot], (it / PDX) & 1, a.status)))
+          break;
         tc_fence_after();
-        const uint32_t a_base = smem_u32(smem + L::off_a + slot * A_STAGE);
-        const uint32_t x_base = smem_u32(smem + L::off_x + slot * L::X_STAGE);
+        const uint32_t a_base = smem_u32(smem + P::off_a + slot * A_STAGE);
+        const uint32_t x_base = smem_u32(smem + P::off_x + xslot * P::X_STAGE);
 #pragma unroll
         for (int c = 0; c < 2; ++c)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            umma_f16(acc, sdesc_k_sw128(a_base + c * A_ATOM + kk * 32), sdesc_k_sw128(x_base + c * L::X_ATOM + kk * 32),
-                     idesc, (s | c | kk) != 0);
+            umma_f16(acc, sdesc_k_sw128(a_base + c * A_ATOM + kk * 32), sdesc_k_sw128(x_base + c * P::X_ATOM + kk * 32),
+                     idesc, ((s - ka) | c | kk) != 0);
         umma_commit(&a_empty[slot]);
+        umma_commit(&x_empty[xslot]);
       }
       if (ok) umma_commit(&acc_full[ab]);
     }
@@ -520,8 +589,9 @@ __global__ void __launch_bounds__(kPThreads, 1)
     const int r = tt >> 1, c = tt & 1;
     int it = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-      for (int s = 0; s < nst; ++s, ++it) {
+    int t, ka, kb;
+    for (first_seg(t, ka, kb); t < tiles && ok; next_seg(t, ka, kb)) {
+      for (int s = ka; s < kb; ++s, ++it) {
         const int rs = it % PDR, as = it % PDA;
         ok = __shfl_sync(0xffffffffu, mbar_wait(&raw_full[rs], (it / PDR) & 1, a.status), 0);
         if (!ok) break;
@@ -562,7 +632,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
     // ---- epilogue ----
     const int q = warp & 3;
     int j = 0;
-    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++j) {
+    int t, ka, kb;
+    for (first_seg(t, ka, kb); t < tiles; next_seg(t, ka, kb), ++j) {
       const int ab = j & 1;
       const bool ok = __shfl_sync(0xffffffffu, mbar_wait(&acc_full[ab], (j >> 1) & 1, a.status), 0);
       if (!ok) break;
@@ -935,11 +1006,11 @@ void launch_bn(const TcGemmArgs& g, cudaStream_t s) {
     attr_set = true;
   }
   dim3 grid(g.N / BM, (g.M + BN - 1) / BN, splits);
-  launch(tc_gemm_q4k_kernel<BN, SW, false>, grid, dim3(kThreads), L::total, s, g.pdl, tm_hdr, tm_qs, tm_x, a);
+  launch(tc_gemm_q4k_kernel<BN, SW, false>, grid, dim3(L::THREADS), L::total, s, g.pdl, tm_hdr, tm_qs, tm_x, a);
 }
 
 template <int BN, bool SW>
-void launch_persistent(const TcGemmArgs& g, cudaStream_t s) {
+void launch_persistent(const TcGemmArgs& g, cudaStream_t s, bool stream_k = false) {
   using P = PLayout<BN>;
   const uint64_t rb = (uint64_t)g.w_row_bytes, hb = (uint64_t)g.w_hdr_row_bytes;
   const uint32_t box_rows = SW ? BM / 2 : BM;
@@ -956,7 +1027,8 @@ void launch_persistent(const TcGemmArgs& g, cudaStream_t s) {
   a.stages_per_split = a.stages_total;
   a.y = g.y;
   a.y_stride = g.y_stride;
-  a.atomic = g.atomic ? 1 : 0;
+  a.atomic = (g.atomic || stream_k) ? 1 : 0;
+  a.stream_k = stream_k ? 1 : 0;
   a.status = g.status;
   a.h = g.h;
   a.h_stride = g.h_stride;
@@ -972,8 +1044,11 @@ void launch_persistent(const TcGemmArgs& g, cudaStream_t s) {
     attr_set = true;
   }
   const int tiles = ((g.M + BN - 1) / BN) * (g.N / BM);
-  launch(tc_gemm_q4k_persistent<BN, SW>, dim3(std::min(tiles, sms)), dim3(kPThreads), P::total, s, g.pdl, tm_hdr,
-         tm_qs, tm_x, a);
+  // stream-K: one CTA per SM (at least 4 K stages each), every CTA the same number of stages
+  // within one; otherwise one CTA per tile up to one per SM
+  const int64_t units = (int64_t)tiles * a.stages_total;
+  const int grid = stream_k ? (int)std::max<int64_t>(1, std::min<int64_t>(sms, units / 4)) : std::min(tiles, sms);
+  launch(tc_gemm_q4k_persistent<BN, SW>, dim3(grid), dim3(kPThreads), P::total, s, g.pdl, tm_hdr, tm_qs, tm_x, a);
 }
 
 // True when the CTA-pair kernel covers the shape (whole 256-row weight pair tiles).
@@ -1068,7 +1143,7 @@ void launch_abf(const TcBf16Args& g, cudaStream_t s) {
   const int ty = g.tiles ? g.max_tiles : (g.M + BN - 1) / BN;
   if (ty <= 0) return;
   dim3 grid((g.N + BM - 1) / BM, ty, splits);
-  launch(tc_gemm_q4k_kernel<BN, SW, true>, grid, dim3(kThreads), L::total, s, g.pdl, tm_a, tm_a, tm_x, a);
+  launch(tc_gemm_q4k_kernel<BN, SW, true>, grid, dim3(L::THREADS), L::total, s, g.pdl, tm_a, tm_a, tm_x, a);
 }
 
 }  // namespace
@@ -1114,6 +1189,16 @@ void tc_gemm_launch(const TcGemmArgs& g, cudaStream_t s) {
   if (g.N % BM) throw std::runtime_error("tc_gemm: N must be a multiple of 128");
   if (g.K % 256) throw std::runtime_error("tc_gemm: K must be a multiple of 256");
   if (g.k_splits > 1 && !g.atomic && !g.y_zeroed) throw std::runtime_error("tc_gemm: split-K needs a zeroed output");
+  if (g.persistent == 2) {  // stream-K: balanced (tile, stage) ranges, partial tiles by atomics
+    if (g.h) throw std::runtime_error("tc_gemm stream-K: no SwiGLU epilogue");
+    if (!g.atomic && !g.y_zeroed) throw std::runtime_error("tc_gemm stream-K: needs a zeroed or accumulated output");
+    switch (g.bn) {
+      case 64: launch_persistent<64, false>(g, s, true); break;
+      case 128: launch_persistent<128, false>(g, s, true); break;
+      default: throw std::runtime_error("tc_gemm stream-K: bn must be 64 or 128");
+    }
+    return;
+  }
   if (g.persistent) {  // prefill-sized M: persistent CTAs, double-buffered TMEM accumulators
     if (g.bn != 256 && g.bn != 128) throw std::runtime_error("tc_gemm persistent: bn must be 128 or 256");
     if (g.h && g.N % 128) throw std::runtime_error("tc_gemm swiglu: F must be a multiple of 64");

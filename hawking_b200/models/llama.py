@@ -762,8 +762,10 @@ class LlamaModel:
         if not wide:  # wide: the O site left norm(x2) in self.xb
             ops.rmsnorm(x, lw.ffn_norm, self.cfg.eps, yb=self.xb[:rows])
         bn = 64 if rows <= 64 else (128 if rows < 192 else 256)
-        if self.fuse_swiglu_tc and F % 64 == 0 and lw.w_gu.N == 2 * F and (F // 64) * -(-rows // bn) >= 148:
-            # SwiGLU in the GEMM epilogue (enough tiles to fill the GPU without split-K)
+        if self.fuse_swiglu_tc and F % 64 == 0 and lw.w_gu.N == 2 * F and (F // 64) * -(-rows // bn) >= 148 \
+                and not ops.tc_gemm_stream_k(rows, lw.w_gu.N):
+            # SwiGLU in the GEMM epilogue (enough tiles to fill the GPU without split-K); decode
+            # batches instead run gate/up stream-K and the SwiGLU kernel (no partial last wave)
             ops.tc_gemm_swiglu(lw.w_gu, self.xb[:rows], self.hb[:rows, :F], self.status, bn=bn)
         else:
             gu = self.gu[:rows, : 2 * F]

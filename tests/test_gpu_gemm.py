@@ -148,3 +148,23 @@ def test_tc_gemm_persistent_repeated_multi_tile(pair, monkeypatch):
         torch.cuda.synchronize()
         assert st.item() == 0
         _check(out, ref)
+
+
+@pytest.mark.parametrize("M,N,K", [(64, 19200, 2304), (17, 28672, 1024), (1, 20480, 512)])
+@pytest.mark.parametrize("residual", [False, True])
+def test_tc_gemm_stream_k(M, N, K, residual):
+    """Stream-K decode-batch GEMM: each CTA takes a balanced range of (weight tile, K stage) units
+    that may start and end inside tiles (150 tiles x 18 stages over 148 CTAs, ...), the partial
+    tiles accumulated with atomics into a zeroed output or onto a residual."""
+    assert ops.tc_gemm_stream_k(M, N)
+    w, x, ref = _case(N, K, M, N + K + M)
+    y0 = torch.randn(M, N, device=DEV) if residual else torch.zeros(M, N, device=DEV)
+    y = y0.clone()
+    st = torch.zeros(1, dtype=torch.int32, device=DEV)
+    if residual:
+        ops.tc_gemm(w, x, y, st, atomic=True)
+    else:
+        ops.tc_gemm(w, x, y, st, y_zeroed=True)
+    torch.cuda.synchronize()
+    assert st.item() == 0
+    _check(y - y0, ref)
