@@ -306,8 +306,40 @@ __global__ void __launch_bounds__(256) swiglu_bf16_kernel(float* gu, int64_t gs,
   pdl_launch();
 }
 
+// Four columns per thread (16-byte loads of g and u, one 8-byte store of h): the prefill-sized
+// SwiGLU (2048 rows x 14336) streams 294 MB, which the one-column kernel above moved at about a
+// third of the HBM rate.
+__global__ void __launch_bounds__(256) swiglu_bf16_v4_kernel(float* gu, int64_t gs, int F, __nv_bfloat16* h,
+                                                              int64_t hs, int clear) {
+  pdl_wait();
+  const int m = blockIdx.y;
+  float4* g = reinterpret_cast<float4*>(gu + (int64_t)m * gs);
+  float4* u = reinterpret_cast<float4*>(gu + (int64_t)m * gs + F);
+  uint2* out = reinterpret_cast<uint2*>(h + (int64_t)m * hs);
+  for (int f = blockIdx.x * blockDim.x + threadIdx.x; f < F / 4; f += gridDim.x * blockDim.x) {
+    const float4 gv = g[f], uv = u[f];
+    const float a0 = gv.x / (1.f + __expf(-gv.x)) * uv.x, a1 = gv.y / (1.f + __expf(-gv.y)) * uv.y;
+    const float a2 = gv.z / (1.f + __expf(-gv.z)) * uv.z, a3 = gv.w / (1.f + __expf(-gv.w)) * uv.w;
+    const __nv_bfloat162 p0 = __floats2bfloat162_rn(a0, a1), p1 = __floats2bfloat162_rn(a2, a3);
+    out[f] = make_uint2(*reinterpret_cast<const uint32_t*>(&p0), *reinterpret_cast<const uint32_t*>(&p1));
+    if (clear) {
+      g[f] = make_float4(0.f, 0.f, 0.f, 0.f);
+      u[f] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+  pdl_launch();
+}
+
 void swiglu_bf16_launch(float* gu, int64_t gu_stride, int M, int F, __nv_bfloat16* h, int64_t h_stride, bool clear,
                         cudaStream_t s, bool pdl) {
+  if (M <= 0) return;
+  const bool v4 = F % 4 == 0 && gu_stride % 4 == 0 && h_stride % 4 == 0 &&
+                  ((reinterpret_cast<uintptr_t>(gu) & 15) | (reinterpret_cast<uintptr_t>(h) & 7)) == 0;
+  if (v4) {
+    dim3 grid(std::min(64, (F / 4 + 255) / 256), M);
+    launch(swiglu_bf16_v4_kernel, grid, dim3(256), 0, s, pdl, gu, gu_stride, F, h, h_stride, (int)clear);
+    return;
+  }
   dim3 grid(std::min(64, (F + 255) / 256), M);
   launch(swiglu_bf16_kernel, grid, dim3(256), 0, s, pdl, gu, gu_stride, F, h, h_stride, (int)clear);
 }

@@ -32,6 +32,9 @@ from ..ops import mg
 from .config import ModelConfig
 
 GEMV_COLS = 8  # rows per GEMV launch (dp4a GEMV batch limit)
+# Prefill-sized FFNs: gate/up with the SwiGLU fused in the persistent GEMM's epilogue (1), or the
+# plain persistent GEMM plus the vectorised SwiGLU kernel (0, default)
+FUSED_SWIGLU_PREFILL = os.environ.get("HK_FUSED_SWIGLU_PREFILL", "0") == "1"
 # RoPE + paged K/V append in the W4A16 QKV GEMV epilogue where the weights allow it
 ROPE_EPI = os.environ.get("HK_ROPE_EPI", "1") == "1"
 # prefill-sized forwards of GGUF formats other than Q4_K run their dense projections as tensor-core
@@ -762,11 +765,20 @@ class LlamaModel:
         if not wide:  # wide: the O site left norm(x2) in self.xb
             ops.rmsnorm(x, lw.ffn_norm, self.cfg.eps, yb=self.xb[:rows])
         bn = 64 if rows <= 64 else (128 if rows < 192 else 256)
+        once = ops.tc_gemm_overwrites(rows)
         if self.fuse_swiglu_tc and F % 64 == 0 and lw.w_gu.N == 2 * F and (F // 64) * -(-rows // bn) >= 148 \
-                and not ops.tc_gemm_stream_k(rows, lw.w_gu.N):
+                and not ops.tc_gemm_stream_k(rows, lw.w_gu.N) and not (once and not FUSED_SWIGLU_PREFILL):
             # SwiGLU in the GEMM epilogue (enough tiles to fill the GPU without split-K); decode
             # batches instead run gate/up stream-K and the SwiGLU kernel (no partial last wave)
             ops.tc_gemm_swiglu(lw.w_gu, self.xb[:rows], self.hb[:rows, :F], self.status, bn=bn)
+        elif once:
+            # prefill-sized: the persistent GEMM stores gate/up (no zeroing) and the SwiGLU kernel
+            # streams them once; it re-zeroes only the rows the split-K paths (< 192 rows) reuse
+            gu = self.gu[:rows, : 2 * F]
+            ops.tc_gemm(lw.w_gu, self.xb[:rows], gu, self.status)
+            keep = min(rows, ops.SPLIT_K_MAX_ROWS)
+            ops.swiglu_bf16(gu[:keep], F, self.hb[:keep, :F], clear=True)
+            ops.swiglu_bf16(gu[keep:], F, self.hb[keep:rows, :F], clear=False)
         else:
             gu = self.gu[:rows, : 2 * F]
             ops.tc_gemm(lw.w_gu, self.xb[:rows], gu, self.status, y_zeroed=True)

@@ -262,10 +262,14 @@ def tc_gemm_stream_k(M: int, N: int) -> bool:
     return STREAM_K and M <= 64 and (N // 128) > SMS
 
 
+# Below this many rows tensor-core GEMMs split K (or run stream-K) into a zeroed output.
+SPLIT_K_MAX_ROWS = 191
+
+
 def tc_gemm_overwrites(M: int) -> bool:
     """Whether a tensor-core GEMM over M rows (engine tile choice) writes every output element
     exactly once with a plain store (the persistent path: no split-K), so y needs no zeroing."""
-    return PERSISTENT_GEMM and M >= 192
+    return PERSISTENT_GEMM and M > SPLIT_K_MAX_ROWS
 
 
 def tc_gemm(w: QWeight, x: torch.Tensor, y: torch.Tensor, status: torch.Tensor, atomic: bool = False,

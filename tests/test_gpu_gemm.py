@@ -168,3 +168,21 @@ def test_tc_gemm_stream_k(M, N, K, residual):
     torch.cuda.synchronize()
     assert st.item() == 0
     _check(y - y0, ref)
+
+
+@pytest.mark.parametrize("M,F,clear", [(300, 14336, False), (5, 512, True), (7, 250, True)])
+def test_swiglu_bf16_kernel(M, F, clear):
+    """h = silu(g) * u as bf16 from the fp32 [g | u] rows (four columns per thread when F and the
+    rows are 16-byte aligned, one otherwise); ``clear`` re-zeroes the rows it read."""
+    g = torch.Generator(device=DEV).manual_seed(M + F)
+    gu = torch.randn(M, 2 * F, device=DEV, generator=g)
+    ref = (torch.nn.functional.silu(gu[:, :F]) * gu[:, F:]).bfloat16().float()
+    h = torch.zeros(M, F, dtype=torch.bfloat16, device=DEV)
+    src = gu.clone()
+    ops.swiglu_bf16(src, F, h, clear=clear)
+    torch.cuda.synchronize()
+    assert (h.float() - ref).abs().max().item() <= 1e-2 * ref.abs().max().item()
+    if clear:
+        assert not src.any()
+    else:
+        assert torch.equal(src, gu)
