@@ -62,8 +62,11 @@ __device__ __forceinline__ uint32_t swz(int row, int c) {
   return (uint32_t)(row * HD * 2 + ((c ^ (row & 7)) << 4));
 }
 
+// Two CTAs per SM (HPC = 2: 16 warps; at most 128 registers per thread): the query fragments are
+// re-read from shared memory per k-step instead of living in registers for the whole kernel
+// (210 registers had left one CTA, 8 warps, per SM).
 template <int HD, int HPC>
-__global__ void __launch_bounds__(128 * HPC) attn_prefill_kernel(AttnDecodeArgs a) {
+__global__ void __launch_bounds__(128 * HPC, HPC == 2 ? 2 : 4) attn_prefill_kernel(AttnDecodeArgs a) {
   constexpr int CH = HD / 8;           // 16-byte chunks per row
   constexpr int TILE = kPfBN * HD * 2;  // bytes of one K or V tile
   constexpr int NT = 128 * HPC;         // threads
@@ -101,14 +104,9 @@ __global__ void __launch_bounds__(128 * HPC) attn_prefill_kernel(AttnDecodeArgs 
     *reinterpret_cast<uint4*>(qs_all + hh * kPfBM * HD * 2 + swz<HD>(row, c)) = v;
   }
   __syncthreads();
-  uint32_t qf[HD / 16][4];
-  {
-    const int mi = lane >> 3;
-    const int row = warp * 16 + (mi & 1) * 8 + (lane & 7);
-#pragma unroll
-    for (int kk = 0; kk < HD / 16; ++kk)
-      ldsm_x4(smem_u32(qs) + swz<HD>(row, kk * 2 + (mi >> 1)), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
-  }
+  // this lane's ldmatrix row of the warp's 16 query rows (A fragments re-read per k-step)
+  const uint32_t q_u = smem_u32(qs);
+  const int q_row = warp * 16 + ((lane >> 3) & 1) * 8 + (lane & 7), q_hi = (lane >> 3) >> 1;
   const float sl2 = a.scale * kLog2e;
   const int lr0 = warp * 16 + (lane >> 2), lr1 = lr0 + 8;  // this thread's two accumulator rows
   const uint32_t ks_u = smem_u32(ks), vs_u = smem_u32(vs);
@@ -166,13 +164,15 @@ __global__ void __launch_bounds__(128 * HPC) attn_prefill_kernel(AttnDecodeArgs 
         const int mi = lane >> 3;
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
+          uint32_t qf[4];
+          ldsm_x4(q_u + swz<HD>(q_row, kk * 2 + q_hi), qf[0], qf[1], qf[2], qf[3]);
 #pragma unroll
           for (int nb2 = 0; nb2 < kPfBN / 16; ++nb2) {
             uint32_t b0, b1, b2, b3;
             const int key = nb2 * 16 + (mi >> 1) * 8 + (lane & 7);
             ldsm_x4(kb + swz<HD>(key, kk * 2 + (mi & 1)), b0, b1, b2, b3);
-            mma_bf16(s[2 * nb2], qf[kk], b0, b1);
-            mma_bf16(s[2 * nb2 + 1], qf[kk], b2, b3);
+            mma_bf16(s[2 * nb2], qf, b0, b1);
+            mma_bf16(s[2 * nb2 + 1], qf, b2, b3);
           }
         }
       }
