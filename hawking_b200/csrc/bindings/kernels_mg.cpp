@@ -170,6 +170,7 @@ void mg_gemv(int64_t fmt, int64_t xin, int64_t epi, const Tensor& tiles, int64_t
     a.block_size = (int)rope_dims[2];
     a.k_cache = ptr<__nv_bfloat16>(kc);
     a.v_cache = ptr<__nv_bfloat16>(vc);
+    a.cache_blocks = kc.size(0);
     a.q_out = rope_epi[6]->data_ptr<float>();
     a.nh = (int)rope_dims[0];
     a.nkv = (int)rope_dims[1];

@@ -173,6 +173,7 @@ void rope_append(const Tensor& qkv, const optional<Tensor>& bias, const optional
   a.block_tables = optr<int>(block_tables);
   a.row_seq = optr<int>(row_seq);
   a.max_blocks = block_tables.has_value() ? (int)block_tables->size(1) : 0;
+  a.cache_blocks = k_cache.size(0);
   TORCH_CHECK(a.slots || (a.block_tables && a.row_seq), "rope_append: slots or block tables required");
   const c10::cuda::CUDAGuard g(qkv.device());
   hk::rope_append_launch(a, cur_stream(), pdl);

@@ -182,6 +182,8 @@ struct MgArgs {
   const int* row_seq;
   const int* block_tables;
   int max_blocks, block_size;
+  int64_t cache_blocks;        // blocks in the caches: a row whose block id or table column is out
+                               // of range skips its K/V append
   __nv_bfloat16* k_cache;
   __nv_bfloat16* v_cache;
   float* q_out;
@@ -293,6 +295,8 @@ struct RopeAppendArgs {
   const int* block_tables;     //   slot from block_tables[row_seq[r], pos / bs] (when slots is null)
   const int* row_seq;
   int max_blocks;
+  int64_t cache_blocks;        // blocks in the caches: a slot outside them (or a position past the
+                               // row's table) skips the append
   const float* rope;           // [max_pos, rot/2, 2] (cos, sin)
   int rot_dim, rope_style;     // 0 adjacent pairs, 1 neox halves
   float* q_out;                // [R, nh, hd] fp32 (roped)

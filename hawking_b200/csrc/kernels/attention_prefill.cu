@@ -119,6 +119,7 @@ __global__ void __launch_bounds__(128 * HPC, HPC == 2 ? 2 : 4) attn_prefill_kern
     while (s1 < nvalid && seq_s[s1] == seq) ++s1;
     int kv_len = 0;
     for (int i = s0; i < s1; ++i) kv_len = max(kv_len, ctx_s[i]);
+    kv_len = min(kv_len, a.max_blocks * a.block_size);  // never past the row's table
     const bool in0 = lr0 >= s0 && lr0 < s1, in1 = lr1 >= s0 && lr1 < s1;
     const int c0 = in0 ? ctx_s[lr0] : 0, c1 = in1 ? ctx_s[lr1] : 0;
     float m0 = NEG, m1 = NEG, l0 = 0.f, l1 = 0.f;

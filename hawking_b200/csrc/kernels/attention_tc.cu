@@ -141,7 +141,7 @@ __global__ void __launch_bounds__(Cfg<NC>::kThreads, 2)
 
   const int ctx = a.row_ctx[r];
   const int* btab = a.block_tables + (int64_t)a.row_seq[r] * a.max_blocks;
-  const int nblk_ctx = (ctx + bs - 1) / bs;
+  const int nblk_ctx = min((ctx + bs - 1) / bs, a.max_blocks);  // never past the row's table
   const int bpc = (nblk_ctx + S - 1) / S;
   const int b0 = split * bpc, b1 = min(nblk_ctx, b0 + bpc);
   const int nb = max(0, b1 - b0);

@@ -138,6 +138,20 @@ void rmsnorm_launch(const float* x, int64_t x_stride, const float* w, float eps,
 }
 
 // ---- RoPE + paged KV append -----------------------------------------------------------------
+// Cache slot of row r (-1: skip the append): the given slot, or block_tables[row_seq[r]] at the
+// position's block; a position past the row's table or a block outside the caches is skipped
+// rather than written out of bounds.
+__device__ __forceinline__ int64_t append_slot(const RopeAppendArgs& a, int r, int pos) {
+  const int64_t limit = a.cache_blocks * a.block_size;
+  if (a.slots) {
+    const int64_t s = a.slots[r];
+    return s >= 0 && s < limit ? s : -1;
+  }
+  if (!a.block_tables || pos < 0 || pos / a.block_size >= a.max_blocks) return -1;
+  const int blk = a.block_tables[(int64_t)a.row_seq[r] * a.max_blocks + pos / a.block_size];
+  return blk >= 0 && blk < a.cache_blocks ? (int64_t)blk * a.block_size + pos % a.block_size : -1;
+}
+
 // Grid (head groups, rows); one warp per head (q heads, then k heads, then v heads), so every
 // head is a single round trip.
 __global__ void __launch_bounds__(256) rope_append_kernel(RopeAppendArgs a) {
@@ -145,11 +159,7 @@ __global__ void __launch_bounds__(256) rope_append_kernel(RopeAppendArgs a) {
   const int r = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   const int pos = a.positions[r];
-  int64_t slot = -1;
-  if (a.slots) slot = a.slots[r];
-  else if (a.block_tables)
-    slot = (int64_t)a.block_tables[(int64_t)a.row_seq[r] * a.max_blocks + pos / a.block_size] * a.block_size +
-           pos % a.block_size;
+  const int64_t slot = append_slot(a, r, pos);
   const int hd = a.hd, half = a.rot_dim / 2;
   const float* rope = a.rope + (int64_t)pos * half * 2;
   const int nheads = a.nh + 2 * a.nkv;
@@ -215,11 +225,7 @@ __global__ void __launch_bounds__(256) rope_append_hd128_kernel(RopeAppendArgs a
   const int r = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   const int pos = a.positions[r];
-  int64_t slot = -1;
-  if (a.slots) slot = a.slots[r];
-  else if (a.block_tables)
-    slot = (int64_t)a.block_tables[(int64_t)a.row_seq[r] * a.max_blocks + pos / a.block_size] * a.block_size +
-           pos % a.block_size;
+  const int64_t slot = append_slot(a, r, pos);
   const float* rope = a.rope + (int64_t)pos * 128;  // 64 (cos, sin) pairs
   const int nheads = a.nh + 2 * a.nkv;
   for (int h = blockIdx.x * nw + warp; h < nheads; h += gridDim.x * nw) {

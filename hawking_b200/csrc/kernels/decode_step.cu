@@ -248,7 +248,8 @@ __device__ __forceinline__ void epilogue(const DsArgs& a, const EpiCtx& e, uint3
   if constexpr (EPI == EPI_QKV) {
     const int64_t layer = (int64_t)e.l * a.num_cache_blocks * a.nkv * a.block_size * a.hd;
     const RopeEpi r{a.rope, a.positions, a.row_seq, a.block_tables, a.max_blocks, a.block_size,
-                    a.k_cache + layer, a.v_cache + layer, a.q, e.qkv_bias, a.nh, a.nkv, a.hd, a.rot, a.rope_style};
+                    a.k_cache + layer, a.v_cache + layer, a.q, e.qkv_bias, a.nh, a.nkv, a.hd, a.rot, a.rope_style,
+                    (int64_t)a.num_cache_blocks};
     rope_epilogue<NB>(r, a.nb, g, v, lane);
   } else if constexpr (EPI == EPI_RESID) {
 #pragma unroll

@@ -251,6 +251,7 @@ struct RopeEpi {
   float* q;                  // [nb, nh, hd]
   const float* bias;         // logical row order; may be null
   int nh, nkv, hd, rot, style;
+  int64_t cache_blocks;      // blocks in the caches (out-of-range appends are skipped)
 };
 
 template <int NB>
@@ -287,7 +288,9 @@ __device__ __forceinline__ void rope_epilogue(const RopeEpi& r, int nb, uint32_t
       __stcg(dst + db, x1);
     } else {
       const int kh = head - r.nh - (kind == 2 ? r.nkv : 0);
+      if (pos < 0 || pos / r.block_size >= r.max_blocks) continue;  // past the row's table: skip
       const int blk = r.block_tables[(int64_t)r.row_seq[col] * r.max_blocks + pos / r.block_size];
+      if (blk < 0 || blk >= r.cache_blocks) continue;
       const int64_t row = ((int64_t)blk * r.nkv + kh) * r.block_size + pos % r.block_size;
       __nv_bfloat16* dst = (kind == 1 ? r.k_cache : r.v_cache) + row * r.hd;
       dst[da] = __float2bfloat16_rn(x0);

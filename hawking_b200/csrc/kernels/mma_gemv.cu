@@ -263,7 +263,7 @@ __device__ __forceinline__ void epilogue(const MgArgs& a, uint32_t g_, const flo
   const int r0 = lane >> 2, q = lane & 3;
   if constexpr (EPI == MG_ROPE) {
     const RopeEpi r{a.rope, a.positions, a.row_seq, a.block_tables, a.max_blocks, a.block_size, a.k_cache,
-                    a.v_cache, a.q_out, a.bias, a.nh, a.nkv, a.rp_hd, a.rp_rot, a.rp_style};
+                    a.v_cache, a.q_out, a.bias, a.nh, a.nkv, a.rp_hd, a.rp_rot, a.rp_style, a.cache_blocks};
     rope_epilogue<2>(r, a.nb, g_, v, lane);
   } else if constexpr (EPI == MG_SWIGLU) {
     const int64_t o = g * 8 + r0;  // output row: gate in tile row r0, up in r0 + 8

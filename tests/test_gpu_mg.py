@@ -224,8 +224,9 @@ def test_mg_rope_epilogue_matches_store_then_rope(hd, rot, style, nb, math):
     rope = ops.rope_table(512, rot, 10000.0, None, DEV)
     positions = torch.tensor([5 + 37 * i for i in range(nb)], dtype=torch.int32, device=DEV)
     row_seq = torch.arange(nb, dtype=torch.int32, device=DEV)
-    nblk = nb * 16 + 4
-    tables = torch.randperm(nblk, device=DEV)[: nb * 16].int().view(nb, 16).contiguous()
+    mb = 20  # table columns: 20 blocks of 16 cover the largest position (5 + 37 * 7 = 264)
+    nblk = nb * mb + 4
+    tables = torch.randperm(nblk, device=DEV)[: nb * mb].int().view(nb, mb).contiguous()
     outs = []
     for fused in (False, True):
         kc = torch.zeros(nblk, nkv, bs, hd, dtype=torch.bfloat16, device=DEV)
