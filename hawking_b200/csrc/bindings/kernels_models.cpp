@@ -31,9 +31,9 @@ Tensor mixed_descs(const std::vector<Tensor>& codes, const std::vector<Tensor>& 
   std::vector<hk::MixedDesc> h(n);
   for (size_t i = 0; i < n; ++i) {
     TORCH_CHECK(codes[i].is_cuda() && codes[i].scalar_type() == at::kByte && codes[i].dim() == 2, "codes: uint8 [rows, bytes]");
-    const bool fp8 = kind[i] == hk::MIXED_FP8;
+    const bool fp8 = kind[i] == hk::MIXED_FP8 || kind[i] == hk::MIXED_FP4;  // fp32 scales
     TORCH_CHECK(scales[i].is_cuda() && scales[i].scalar_type() == (fp8 ? at::kFloat : at::kHalf) && scales[i].dim() == 2,
-                "scales: fp16 (fp32 for fp8) [rows, groups]");
+                "scales: fp16 (fp32 for fp8 / fp4) [rows, groups]");
     TORCH_CHECK((reinterpret_cast<uintptr_t>(codes[i].data_ptr()) & 15) == 0 && codes[i].stride(0) % 16 == 0,
                 "codes rows must be 16-byte aligned");
     h[i].codes = ptr<uint8_t>(codes[i]);
@@ -49,10 +49,11 @@ Tensor mixed_descs(const std::vector<Tensor>& codes, const std::vector<Tensor>& 
                                                                                     : (1 << (bits[i] - 1)) - 1)
                                               : 0;
     TORCH_CHECK(kind[i] == hk::MIXED_BINARY ? bits[i] == 1
-                                            : (kind[i] == hk::MIXED_FP8 || kind[i] == hk::MIXED_Q4K
+                                            : (kind[i] == hk::MIXED_FP8 || kind[i] == hk::MIXED_Q4K || kind[i] == hk::MIXED_FP4
                                                    ? bits[i] == (kind[i] == hk::MIXED_FP8 ? 8 : 4)
                                                    : (bits[i] == 2 || bits[i] == 4 || bits[i] == 8)),
-                "mixed codec: binary (1 bit), uniform 2/4/8 bits, fp8 (8 bits) or Q4_K (4 bits)");
+                "mixed codec: binary (1 bit), uniform 2/4/8 bits, fp8 (8 bits), Q4_K or fp4 (4 bits)");
+    TORCH_CHECK(kind[i] != hk::MIXED_FP4 || group[i] == 32, "mixed fp4: one scale per 32 columns");
     TORCH_CHECK(group[i] % 32 == 0, "mixed codec: group must be a multiple of 32");
     TORCH_CHECK(kind[i] != hk::MIXED_Q4K || (group[i] == 256 && scales[i].stride(0) % 8 == 0 &&
                                              (reinterpret_cast<uintptr_t>(scales[i].data_ptr()) & 15) == 0),

@@ -525,11 +525,13 @@ void moe_gemv_launch(int fmt, int epi, const MoeGemvArgs& a, cudaStream_t s, boo
 // ---- `.gravity` mixed low-bit codecs (mixed_gemv.cu) ----
 // MIXED_Q4K: a GGUF Q4_K tensor as its two planes (quants [rows, K/2] as codes, the 16-byte
 // super-block headers d | dmin | 12 scale bytes as `scales`, [rows, K/32] halves)
-enum MixedKind : int { MIXED_BINARY = 0, MIXED_UNIFORM = 1, MIXED_FP8 = 2, MIXED_Q4K = 3 };
+// MIXED_FP4: fp4 e2m1 codes two per byte (even column in the low nibble, [rows, K/2]) with one
+// power-of-two scale per 32 columns (the e8m0 exponents, exact as fp32: scales_f32 [rows, K/32])
+enum MixedKind : int { MIXED_BINARY = 0, MIXED_UNIFORM = 1, MIXED_FP8 = 2, MIXED_Q4K = 3, MIXED_FP4 = 4 };
 struct MixedDesc {            // one weight tensor [rows, K] in device memory
   const uint8_t* codes;       // LSB-first code stream per row
   const __half* scales;       // fp16 group scales per row (binary / uniform)
-  const float* scales_f32;    // fp8: fp32 scale per (row, group of columns)
+  const float* scales_f32;    // fp8 / fp4: fp32 scale per (row, group of columns)
   int64_t code_row_bytes;     // K * bits / 8
   int64_t scale_row_elems;    // K / group
   int kind, bits, group, bound;

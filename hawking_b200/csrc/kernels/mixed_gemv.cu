@@ -1,6 +1,7 @@
 // `.gravity` sub-2-bit / low-bit GEMV (K8): binary sign + group scale (HGRAVB01) and uniform
 // 2/4/8-bit group codes (HGRAVU01; 2-bit with bound 1 is the ternary point), dequantised in
-// registers against q8 activation blocks with dp4a.
+// registers against q8 activation blocks with dp4a; block-scaled fp8 e4m3 and fp4 e2m1 (e8m0
+// exponents per 32 columns) decoded to fp32 against the same blocks.
 //
 // Storage on the GPU is the codec's own payload bytes, split into two planes per tensor: the
 // LSB-first code stream of every row ([rows, K * bits / 8] bytes, exactly the body bits) and the
@@ -61,6 +62,19 @@ __device__ __forceinline__ float mixed_block_dot(const MixedDesc& t, int64_t row
       const uint32_t qw = (uint32_t)q[j];
       acc += a.x * (float)(int8_t)(qw & 0xFF) + a.y * (float)(int8_t)((qw >> 8) & 0xFF) +
              b.x * (float)(int8_t)((qw >> 16) & 0xFF) + b.y * (float)(int8_t)(qw >> 24);
+    }
+    (void)sx;
+    return sw * dx * acc;
+  }
+  if (t.kind == MIXED_FP4) {  // e2m1 codes, element k of a word in nibble k; fp32 scale per block
+    const float sw = t.scales_f32[row * t.scale_row_elems + blk];
+    const uint4 w = __ldg(reinterpret_cast<const uint4*>(codes) + blk);
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+    float acc = 0.f;
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+      const uint32_t c = (ws[e >> 3] >> (4 * (e & 7))) & 0xFu;
+      acc += e2m1_value(c) * (float)(int8_t)(((uint32_t)q[e >> 2] >> (8 * (e & 3))) & 0xFFu);
     }
     (void)sx;
     return sw * dx * acc;

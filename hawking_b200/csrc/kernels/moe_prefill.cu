@@ -38,6 +38,16 @@ __device__ __forceinline__ void mixed_block_values(const MixedDesc& t, int64_t r
     }
     return;
   }
+  if (t.kind == MIXED_FP4) {
+    const float sw = t.scales_f32[row * t.scale_row_elems + blk];
+#pragma unroll
+    for (int i = 0; i < 32; i += 2) {
+      const uint32_t b = codes[blk * 16 + i / 2];
+      v[i] = e2m1_value(b & 0xFu) * sw;
+      v[i + 1] = e2m1_value(b >> 4) * sw;
+    }
+    return;
+  }
   if (t.kind == MIXED_Q4K) {
     const int sb = blk >> 3, j = blk & 7;
     const uint4 h = *(reinterpret_cast<const uint4*>(t.scales + row * t.scale_row_elems) + sb);

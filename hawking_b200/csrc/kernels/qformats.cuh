@@ -19,6 +19,16 @@
 
 namespace hk {
 
+// fp4 e2m1 code (sign | 2 exponent bits | 1 mantissa bit, exponent bias 1) as fp32, built from its
+// bits: exponent 0 is the subnormal m * 0.5, otherwise 2^(e - 1) * (1 + m / 2); the magnitudes
+// are 0, 0.5, 1, 1.5, 2, 3, 4, 6.
+__device__ __forceinline__ float e2m1_value(uint32_t c) {
+  const uint32_t e = (c >> 1) & 3u, m = c & 1u;
+  const uint32_t mag = e ? (((e + 126u) << 23) | (m << 22)) : (m ? (126u << 23) : 0u);
+  return __uint_as_float(mag | ((c & 8u) << 28));
+}
+
+
 
 // Activation loads use generic addressing: the q8 input may live in global or shared memory.
 __device__ __forceinline__ int4 ldx16(const int8_t* p) { return *reinterpret_cast<const int4*>(p); }

@@ -19,7 +19,19 @@ import torch
 
 from .._ext import kernels
 
-BINARY, UNIFORM, FP8, Q4K = 0, 1, 2, 3  # Q4K: a GGUF Q4_K tensor's quant + header planes
+BINARY, UNIFORM, FP8, Q4K, FP4 = 0, 1, 2, 3, 4  # Q4K: a GGUF Q4_K tensor's quant + header planes
+# FP4: e2m1 codes two per byte (even column in the low nibble) with a power-of-two (e8m0) scale
+# per 32 columns, stored as fp32
+
+# e2m1 magnitudes of codes 0..7 (bit 3 is the sign): exponent 0 is subnormal (m / 2), otherwise
+# 2^(e - 1) (1 + m / 2)
+E2M1_MAGNITUDES = (0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0)
+
+
+def e2m1_decode(codes: torch.Tensor) -> torch.Tensor:
+    """fp32 values of 4-bit e2m1 codes (any integer tensor of values 0..15)."""
+    mag = torch.tensor(E2M1_MAGNITUDES, device=codes.device)[(codes & 7).long()]
+    return torch.where((codes & 8) != 0, -mag, mag)
 
 
 def _pack_lsb(codes: torch.Tensor, bits: int) -> torch.Tensor:
@@ -96,6 +108,39 @@ class MixedWeight:
         q = (tiles / sc[:, None, :, None]).view(nbr * block, K)[:N].to(torch.float8_e4m3fn)
         scales = sc.repeat_interleave(block, 0)[:N].contiguous()
         return MixedWeight(FP8, 8, block, N, K, q.view(torch.uint8).contiguous(), scales)
+
+    @staticmethod
+    def quantize_fp4(w: torch.Tensor) -> "MixedWeight":
+        """fp4 e2m1 with one power-of-two scale per 32 columns (the MX rule: the scale is
+        2^(floor(log2 amax) - 2), 2 being the largest e2m1 exponent, and each element takes the
+        nearest e2m1 value of w / scale, saturated at +-6; exactly halfway values take the even
+        code)."""
+        N, K = w.shape
+        if K % 32:
+            raise ValueError("fp4: K must be a multiple of 32")
+        g = w.float().reshape(N, K // 32, 32)
+        amax = g.abs().amax(-1)
+        e = torch.where(amax > 0, torch.floor(torch.log2(amax)) - 2, torch.full_like(amax, -127.0)).clamp(-127, 127)
+        scale = torch.exp2(e)
+        x = (g / scale.unsqueeze(-1)).clamp(-6.0, 6.0)
+        grid = torch.tensor(E2M1_MAGNITUDES, device=w.device)
+        dist = (x.abs().unsqueeze(-1) - grid).abs()
+        # nearest magnitude; ties to the even code (the lower one here: codes 2i are even)
+        idx = torch.argmin(dist + 1e-6 * (torch.arange(8, device=w.device) & 1), dim=-1)
+        codes = (idx | ((x < 0) & (idx > 0)).long() << 3).to(torch.uint8).reshape(N, K)
+        return MixedWeight(FP4, 4, 32, N, K, _pack_lsb(codes, 4).contiguous(), scale.float().contiguous())
+
+    @staticmethod
+    def from_e2m1_e8m0(packed: torch.Tensor, e8m0: torch.Tensor, N: int, K: int, device) -> "MixedWeight":
+        """The source layout of fp4 weights: packed e2m1 pairs [N, K/2] (column c in byte c / 2, the
+        high nibble for odd c) and e8m0 exponents [N, K/32] (scale 2^(e - 127)); the codes are kept
+        as they are and the exponents become exact fp32 scales."""
+        packed = packed.reshape(N, K // 2).to(torch.uint8)
+        e = e8m0.reshape(N, K // 32).to(torch.int32)
+        if bool((e == 255).any()):
+            raise ValueError("fp4: e8m0 exponent 255 (NaN) in the scales")
+        scale = torch.exp2((e - 127).float())
+        return MixedWeight(FP4, 4, 32, N, K, packed.to(device).contiguous(), scale.to(device).contiguous())
 
     @staticmethod
     def random_fp8(N: int, K: int, std: float, gen: torch.Generator, device, block: int = 128,
@@ -188,6 +233,8 @@ class MixedWeight:
             return quant_torch.dequantize(raw, GgmlType.Q4_K, (self.N, self.K)).float()
         if self.kind == FP8:
             return self.codes.view(torch.float8_e4m3fn).float() * self.scales.repeat_interleave(self.group, 1)
+        if self.kind == FP4:
+            return e2m1_decode(_unpack_lsb(self.codes, 4, self.K)) * self.scales.repeat_interleave(32, 1)
         c = _unpack_lsb(self.codes, self.bits, self.K).float()
         s = self.scales.float().repeat_interleave(self.group, 1)
         if self.kind == BINARY:

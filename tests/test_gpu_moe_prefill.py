@@ -20,7 +20,7 @@ def test_table_decode_to_bf16_every_kind():
     g = _g(1)
     w = torch.randn(64, 512, generator=g, device=DEV) * 0.05
     ws = [MixedWeight.quantize(w, BINARY, 1), MixedWeight.quantize(w, UNIFORM, 2), MixedWeight.quantize(w, UNIFORM, 4),
-          MixedWeight.quantize(w, UNIFORM, 8), MixedWeight.quantize_fp8(w)]
+          MixedWeight.quantize(w, UNIFORM, 8), MixedWeight.quantize_fp8(w), MixedWeight.quantize_fp4(w)]
     t = MixedTable(ws)
     out = torch.zeros(64 * len(ws), 512, dtype=torch.bfloat16, device=DEV)
     didx = torch.arange(len(ws), dtype=torch.int32, device=DEV)
