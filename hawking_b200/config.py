@@ -22,6 +22,20 @@ ENV_FLAGS = {
     "HK_BOUNDS": ("0", "build time: compile index guards into the kernels (setup.py)"),
     "HK_SKIP_CUDA": ("0", "build time: build only the host (C++) module"),
     "HK_STARTUP_TIMING": ("0", "Engine.from_gguf prints its load phases (open, config, weights, engine) as JSON"),
+    "HK_SMALL_BATCH": ("w4a16", "decode GEMVs of <= 8 rows: w4a16 (bf16 activations, tensor cores) or w4a8 (int8 blocks, dp4a)"),
+    "HK_MG_MATH": ("int", "W4A16 GEMV math: int (two int8 limbs per activation) or bf16"),
+    "HK_MG_PER_SM": ("max", "W4A16 GEMV CTAs per SM (1..3; fewer leave room for the next kernel's programmatic launch)"),
+    "HK_ROPE_EPI": ("1", "RoPE and the paged K/V append in the QKV GEMV epilogue (0: separate kernel)"),
+    "HK_DSTEP": ("0", "1: the persistent one-launch decode step for <= 4 rows (measured slower; opt-in)"),
+    "HK_DS_WAIT_NS": ("0", "persistent decode step: nanosleep between polls of a grid-barrier flag"),
+    "HK_ATTN_TC": ("1", "decode attention on the tensor cores (0: the CUDA-core cluster kernel)"),
+    "HK_ATTN_STAGES": ("4", "tensor-core decode attention ring stages for one-wave launches (2 or 4)"),
+    "HK_ATTN_PREFETCH_MB": ("48", "L2 prefetch budget of one decode-attention launch, split evenly over its CTAs"),
+    "HK_STREAM_K": ("1", "decode-batch Q4_K GEMMs with more weight tiles than SMs run stream-K (0: one-tile split-K)"),
+    "HK_FUSED_SWIGLU_PREFILL": ("0", "prefill FFN gate/up with the SwiGLU in the GEMM epilogue (0: plain GEMM + SwiGLU kernel)"),
+    "HK_WIDE_GGUF": ("1", "MoE GGUF models: attention projections of forwards above 32 rows as tensor-core GEMMs"),
+    "HK_MOE_PREFILL": ("1", "MoE layers of prefill-sized forwards run grouped tensor-core expert GEMMs"),
+    "HK_TP_WAIT_NS": ("0", "tensor-parallel push all-reduce: nanosleep between polls of a peer flag"),
     "NCCL_NVLS_ENABLE": ("library default", "NCCL NVLink SHARP; the multi-GPU tests set 0"),
 }
 

@@ -89,3 +89,20 @@ def test_gather_window_waits_only_with_free_slots(native):
     eng.work = False
     loop.iterate(idle_wait_ms=7)      # idle: the idle poll
     assert waits[-1] == 7
+
+
+def test_every_runtime_env_flag_is_documented():
+    """Every HK_* variable the package reads at run time (os.environ / getenv) has an entry in
+    ENV_FLAGS with its default and meaning."""
+    import pathlib
+    import re
+
+    from hawking_b200.config import ENV_FLAGS
+    root = pathlib.Path(__file__).resolve().parent.parent / "hawking_b200"
+    pat = re.compile(r'(?:environ\.get\(|getenv\()\s*"(HK_[A-Z0-9_]+)"')
+    read = set()
+    for f in list(root.rglob("*.py")) + list(root.rglob("*.cu")) + list(root.rglob("*.cpp")):
+        read |= set(pat.findall(f.read_text(errors="ignore")))
+    assert read, "no flags found: the pattern is stale"
+    missing = sorted(read - set(ENV_FLAGS))
+    assert not missing, missing
