@@ -397,9 +397,15 @@ __global__ void __launch_bounds__(OLayout<BN>::THREADS, 1)
   }
 }
 
-// ---- persistent variant (prefill-sized M, no split-K) ------------------------------------------
+// ---- persistent variant (prefill-sized M, no split-K; stream-K for decode batches) --------------
 // One CTA per SM walks the tiles t = blockIdx.x, + gridDim.x, ... (weight tile major, token tile
-// minor, so the CTAs in flight share weight tiles in L2). Every role runs its own loop over the
+// minor, so the CTAs in flight share weight tiles in L2). Stream-K mode (TcArgs.stream_k, decode
+// batches whose launch has more weight tiles than SMs): CTA b instead walks the units
+// [b U / G, (b + 1) U / G) of the U = tiles x K-stages (tile major), i.e. a partial tile, whole
+// tiles, a partial tile; every segment gets its own accumulator buffer and the epilogue adds it
+// into y with atomics (zeroed or residual y), so no launch ends in a partial wave of whole tiles.
+// The activation tile has a ring of its own (released by the MMA's commit, as in the one-tile
+// kernel). Every role runs its own loop over the
 // same tile sequence with stage counters that continue across tiles, and the accumulator is
 // double-buffered in TMEM (2 x BN columns): the four dedicated epilogue warps drain tile j while
 // the issuer and the dequantisers already fill tile j + 1, so neither the epilogue nor a partial
