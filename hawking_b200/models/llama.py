@@ -764,7 +764,7 @@ class LlamaModel:
         F = lw.w_down.K
         if not wide:  # wide: the O site left norm(x2) in self.xb
             ops.rmsnorm(x, lw.ffn_norm, self.cfg.eps, yb=self.xb[:rows])
-        bn = 64 if rows <= 64 else (128 if rows < 192 else 256)
+        bn = max(64, ops.tc_gemm_bn(rows))
         once = ops.tc_gemm_overwrites(rows)
         if self.fuse_swiglu_tc and F % 64 == 0 and lw.w_gu.N == 2 * F and (F // 64) * -(-rows // bn) >= 148 \
                 and not ops.tc_gemm_stream_k(rows, lw.w_gu.N) and not (once and not FUSED_SWIGLU_PREFILL):

@@ -266,6 +266,12 @@ def tc_gemm_stream_k(M: int, N: int) -> bool:
 SPLIT_K_MAX_ROWS = 191
 
 
+def tc_gemm_bn(M: int) -> int:
+    """The engine's token tile for a tensor-core GEMM over M rows (256 from SPLIT_K_MAX_ROWS + 1
+    rows up: prefill-sized tiles halve the dequantisation per FLOP and run persistent)."""
+    return 32 if M <= 32 else (64 if M <= 64 else (128 if M <= SPLIT_K_MAX_ROWS else 256))
+
+
 def tc_gemm_overwrites(M: int) -> bool:
     """Whether a tensor-core GEMM over M rows (engine tile choice) writes every output element
     exactly once with a plain store (the persistent path: no split-K), so y needs no zeroing."""
@@ -280,8 +286,7 @@ def tc_gemm(w: QWeight, x: torch.Tensor, y: torch.Tensor, status: torch.Tensor, 
     so unless ``atomic`` (residual add) the caller passes a zeroed ``y`` and ``y_zeroed=True``."""
     M = x.shape[0]
     if bn == 0:
-        # prefill-sized M: 256-token tiles halve the dequantisation per FLOP
-        bn = 32 if M <= 32 else (64 if M <= 64 else (128 if M < 192 else 256))
+        bn = tc_gemm_bn(M)
     persistent = bn == 256 and k_splits in (0, None, 1) and PERSISTENT_GEMM
     stream_k = (not persistent and k_splits in (0, None) and (atomic or y_zeroed) and tc_gemm_stream_k(M, w.N)
                 and w.K % 256 == 0)
@@ -301,7 +306,7 @@ def tc_gemm_swiglu(w_gu: QWeight, x: torch.Tensor, h: torch.Tensor, status: torc
     (2F rows) in one tensor-core launch (the SwiGLU runs in the GEMM epilogue)."""
     M = x.shape[0]
     if bn == 0:
-        bn = 64 if M <= 64 else (128 if M < 192 else 256)
+        bn = max(64, tc_gemm_bn(M))
     launches.add()
     kernels().tc_gemm(w_gu.fmt, w_gu.planes, w_gu.N, w_gu.K, x, h, False, False, 1, bn, status, PDL, h=h,
                       persistent=bn == 256 and PERSISTENT_GEMM)

@@ -106,3 +106,17 @@ def test_every_runtime_env_flag_is_documented():
     assert read, "no flags found: the pattern is stale"
     missing = sorted(read - set(ENV_FLAGS))
     assert not missing, missing
+
+
+def test_tensor_core_gemm_row_regimes_agree():
+    """Below SPLIT_K_MAX_ROWS + 1 rows the tensor-core GEMMs accumulate into a zeroed output
+    (split-K or stream-K), from there on the persistent 256-token tiles overwrite it: the prefill
+    SwiGLU re-zeroes exactly the gate/up rows the smaller forwards reuse, so the three rules must
+    switch at the same row count."""
+    from hawking_b200 import ops
+    for M in range(1, 600):
+        persistent = ops.tc_gemm_bn(M) == 256
+        assert ops.tc_gemm_overwrites(M) == (persistent and ops.PERSISTENT_GEMM), M
+        assert persistent == (M > ops.SPLIT_K_MAX_ROWS), M
+        if ops.tc_gemm_stream_k(M, 28672):
+            assert not persistent and M <= 64
