@@ -450,6 +450,7 @@ bool attention_decode_tc_supported(const AttnDecodeArgs& a) {
 }
 
 void attention_decode_tc_launch(const AttnDecodeArgs& a, int64_t cache_rows, cudaStream_t s, bool pdl) {
+  if (a.R <= 0) return;  // no rows: nothing to launch (and no per-CTA prefetch share to compute)
   if (!attention_decode_tc_supported(a)) throw std::runtime_error("attention (tensor cores): unsupported shape");
   if ((reinterpret_cast<uintptr_t>(a.k_cache) | reinterpret_cast<uintptr_t>(a.v_cache)) & 15)
     throw std::runtime_error("attention (tensor cores): K/V caches must be 16-byte aligned");
