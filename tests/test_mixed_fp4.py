@@ -48,3 +48,15 @@ def test_mx_quantisation_rule():
     assert ((d - w).abs() < 2 * s).all()
     # inputs already on the grid come back exactly
     assert torch.equal(MixedWeight.quantize_fp4(d).dequantize(), d)
+
+
+def test_halfway_values_take_the_even_code():
+    # amax 4 -> scale 2^(2 - 2) = 1; each value sits halfway between two e2m1 neighbours
+    vals = [0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0, 4.0]
+    w = torch.tensor(vals + [0.0] * 24).view(1, 32)
+    m = MixedWeight.quantize_fp4(w)
+    assert m.scales.tolist() == [[1.0]]
+    got = m.dequantize()[0, :8].tolist()
+    assert got == [0.0, 1.0, 1.0, 2.0, 2.0, 4.0, 4.0, 4.0]
+    neg = MixedWeight.quantize_fp4(-w).dequantize()[0, :8].tolist()
+    assert neg == [-0.0 if x == 0 else -x for x in got]
