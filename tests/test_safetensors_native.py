@@ -1,0 +1,85 @@
+"""safetensors container and the native block-scaled pairs of DeepSeek-V4-style checkpoints on the
+host: the container round trip, the pairing rules (fp4 I8 + E8M0 per 32 columns, fp8 E4M3 + E8M0
+per 128 x 128 block) with their refusals, and the values the loaded mixed weights decode to."""
+import numpy as np
+import pytest
+import torch
+
+from hawking_b200.formats.safetensors import (SafeTensors, SafetensorsError, load_native_pair,
+                                              native_scale_pairs, write_safetensors)
+from hawking_b200.ops.mixed import FP4, FP8, _pack_lsb, e2m1_decode
+
+
+def _fp4(N, K, g):
+    codes = torch.randint(0, 16, (N, K), generator=g, dtype=torch.uint8)
+    e = torch.randint(110, 135, (N, K // 32), generator=g, dtype=torch.uint8)
+    return codes, e
+
+
+def _file(tmp_path, tensors, name="m.safetensors"):
+    return SafeTensors(write_safetensors(str(tmp_path / name), tensors, {"format": "pt"}))
+
+
+def test_container_round_trip(tmp_path):
+    a = np.arange(12, dtype=np.float32).reshape(3, 4)
+    st = _file(tmp_path, {"a": ("F32", (3, 4), a.tobytes()), "b": ("U8", (5,), bytes(range(5)))})
+    assert st.names() == ["a", "b"] and st.metadata == {"format": "pt"}
+    assert np.array_equal(st.raw("a").view(np.float32).reshape(3, 4), a)
+    assert bytes(st.raw("b")) == bytes(range(5))
+
+
+def test_native_pairs_load_to_their_values(tmp_path):
+    g = torch.Generator().manual_seed(0)
+    codes, e4 = _fp4(64, 256, g)
+    w8 = (torch.randn(256, 384, generator=g) * 3).to(torch.float8_e4m3fn)
+    e8 = torch.randint(115, 130, (2, 3), generator=g, dtype=torch.uint8)
+    st = _file(tmp_path, {
+        "layers.0.ffn.experts.0.w1.weight": ("I8", (64, 128), _pack_lsb(codes, 4).numpy().tobytes()),
+        "layers.0.ffn.experts.0.w1.scale": ("F8_E8M0", (64, 8), e4.numpy().tobytes()),
+        "layers.0.attn.wq.weight": ("F8_E4M3", (256, 384), w8.view(torch.uint8).numpy().tobytes()),
+        "layers.0.attn.wq.scale": ("F8_E8M0", (2, 3), e8.numpy().tobytes()),
+        "layers.0.attn_norm.weight": ("F32", (4,), np.ones(4, np.float32).tobytes()),
+    })
+    pairs = native_scale_pairs(st)
+    assert set(pairs) == {"layers.0.ffn.experts.0.w1.weight", "layers.0.attn.wq.weight"}
+    p4 = pairs["layers.0.ffn.experts.0.w1.weight"]
+    assert (p4.logical_k, p4.scale_cols) == (256, 8)
+    m4 = load_native_pair(st, p4, "cpu")
+    assert m4.kind == FP4 and (m4.N, m4.K) == (64, 256)
+    ref4 = e2m1_decode(codes) * torch.exp2(e4.float() - 127).repeat_interleave(32, 1)
+    assert torch.equal(m4.dequantize(), ref4)
+    m8 = load_native_pair(st, pairs["layers.0.attn.wq.weight"], "cpu")
+    assert m8.kind == FP8 and (m8.N, m8.K) == (256, 384)
+    blk = torch.exp2(e8.float() - 127).repeat_interleave(128, 0).repeat_interleave(128, 1)
+    assert torch.equal(m8.dequantize(), w8.float() * blk)
+
+
+@pytest.mark.parametrize("case", ["missing_scale", "bad_shape", "orphan_scale", "name", "fp8_dims", "rank"])
+def test_native_pair_refusals(tmp_path, case):
+    w = ("I8", (4, 16), bytes(64))
+    s = ("F8_E8M0", (4, 1), bytes([127] * 4))
+    t = {"x.weight": w, "x.scale": s}
+    if case == "missing_scale":
+        del t["x.scale"]
+    elif case == "bad_shape":
+        t["x.scale"] = ("F8_E8M0", (4, 2), bytes([127] * 8))
+    elif case == "orphan_scale":
+        t["y.scale"] = ("F8_E8M0", (1, 1), bytes([127]))
+    elif case == "name":
+        t = {"x.w": w, "x.scale": s}
+    elif case == "fp8_dims":
+        t = {"x.weight": ("F8_E4M3", (100, 128), bytes(100 * 128)), "x.scale": ("F8_E8M0", (1, 1), bytes([127]))}
+    elif case == "rank":
+        t["x.scale"] = ("F8_E8M0", (4,), bytes([127] * 4))
+    with pytest.raises(SafetensorsError):
+        native_scale_pairs(_file(tmp_path, t))
+
+
+def test_corrupt_offsets_are_refused(tmp_path):
+    import json
+    import struct
+    p = tmp_path / "bad.safetensors"
+    hdr = json.dumps({"a": {"dtype": "F32", "shape": [4], "data_offsets": [0, 12]}}).encode()
+    p.write_bytes(struct.pack("<Q", len(hdr)) + hdr + bytes(16))
+    with pytest.raises(SafetensorsError):
+        SafeTensors(str(p))
