@@ -16,6 +16,8 @@ Native pairs: a tensor ``<stem>.weight`` of dtype ``I8`` or ``F8_E4M3`` is paire
 A weight whose scale is missing, not rank-two E8M0 or not of the exact shape, a weight name that
 does not end in ``.weight``, and an E8M0 tensor that no weight claims are errors. The pairs load
 as mixed-table weights (kinds FP4 and FP8) with the exponents as exact fp32 scales (2^(e - 127)).
+``act_quant_e8m0`` and ``fp8_block_matvec`` state the source checkpoint's own fp8 linear (e4m3
+activations with a power-of-two scale per 128 columns) as a host reference.
 
 Parity: crates/hawking-core/src/gravity_deepseek_v4.rs:114-160 (NativeScalePairKind /
 NativeScalePairGeometry) and :2036-2125 (validate_native_scale_pairs).
@@ -192,3 +194,51 @@ def load_native_pair(st: SafeTensors, pair: NativePair, device):
     rows = sc.repeat_interleave(FP8_BLOCK, 0).contiguous()  # [out, K / 128]
     return MixedWeight(FP8, 8, FP8_BLOCK, pair.out_rows, pair.logical_k, codes.to(device).contiguous(),
                        rows.to(device))
+
+
+# ---- block-scaled activation quantisation of the native fp8 linears --------------------------
+ACT_BLOCK = 128          # activation columns per e8m0 scale
+E4M3_MAX = 448.0
+ACT_AMAX_FLOOR = 1.0e-4  # a block's absolute maximum is raised to this before its scale is taken
+
+
+def act_quant_e8m0(x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Quantise activation rows [..., K] (K % 128 == 0) the way the native fp8 linears expect:
+    per block of 128 columns the scale is the power of two at or above max(amax, 1e-4) * (1 / 448)
+    (the fp32 product; the power from its exponent bits, one up when the mantissa is nonzero),
+    stored as its e8m0 byte, and each element is x / scale clamped to +-448 and rounded to fp8
+    e4m3 (nearest, ties to even). Returns (e4m3 bytes [..., K] uint8, e8m0 bytes [..., K / 128]).
+
+    Parity: crates/hawking-core/src/gravity_deepseek_v4_act_quant.rs:221-300
+    (rounded_ue8m0_scale_byte, act_quant_bf16_ue8m0)."""
+    xf = x.float()
+    K = xf.shape[-1]
+    if K % ACT_BLOCK:
+        raise ValueError("act_quant_e8m0: K must be a multiple of 128")
+    if not bool(torch.isfinite(xf).all()):
+        raise ValueError("act_quant_e8m0: non-finite activation")
+    blocks = xf.reshape(*xf.shape[:-1], K // ACT_BLOCK, ACT_BLOCK)
+    amax = blocks.abs().amax(-1).clamp_min(ACT_AMAX_FLOOR)
+    scaled = amax * torch.tensor(1.0 / E4M3_MAX, dtype=torch.float32)   # the fp32 product
+    bits = scaled.contiguous().view(torch.int32)
+    exp = ((bits >> 23) & 0xFF) - 127 + ((bits & 0x7FFFFF) != 0).to(torch.int32)
+    e8 = exp + 127
+    if bool(((e8 < 0) | (e8 > 254)).any()):
+        raise ValueError("act_quant_e8m0: scale outside the finite e8m0 range")
+    scale = torch.exp2(exp.float())
+    q = (blocks / scale.unsqueeze(-1)).clamp(-E4M3_MAX, E4M3_MAX).to(torch.float8_e4m3fn)
+    return q.view(torch.uint8).reshape(xf.shape), e8.to(torch.uint8)
+
+
+def fp8_block_matvec(w_e4m3: torch.Tensor, w_e8m0: torch.Tensor, a_e4m3: torch.Tensor, a_e8m0: torch.Tensor
+                     ) -> torch.Tensor:
+    """y [rows] of a native fp8 weight ([rows, K] e4m3 bytes, e8m0 [rows / 128, K / 128]) times one
+    quantised activation row (e4m3 bytes [K], e8m0 [K / 128]): per 128-column block the fp32 dot
+    of the decoded codes times the product of the two scales, summed over the blocks in order."""
+    rows, K = w_e4m3.shape
+    w = w_e4m3.view(torch.float8_e4m3fn).float().view(rows, K // ACT_BLOCK, ACT_BLOCK)
+    a = a_e4m3.view(torch.float8_e4m3fn).float().view(K // ACT_BLOCK, ACT_BLOCK)
+    ws = torch.exp2(w_e8m0.float() - 127).repeat_interleave(FP8_BLOCK, 0)[:rows]   # [rows, K / 128]
+    sa = torch.exp2(a_e8m0.float() - 127)                                         # [K / 128]
+    dots = (w * a.unsqueeze(0)).sum(-1)                                           # [rows, K / 128]
+    return (dots * (ws * sa.unsqueeze(0))).sum(-1)

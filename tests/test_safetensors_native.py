@@ -83,3 +83,34 @@ def test_corrupt_offsets_are_refused(tmp_path):
     p.write_bytes(struct.pack("<Q", len(hdr)) + hdr + bytes(16))
     with pytest.raises(SafetensorsError):
         SafeTensors(str(p))
+
+
+def test_act_quant_scale_rule_and_values():
+    from hawking_b200.formats.safetensors import act_quant_e8m0
+    x = torch.zeros(3, 256)
+    x[0, 0] = 448.0           # scaled 1.0: a power of two, e = 0
+    x[0, 128] = 449.0         # just above: e = 1
+    x[1, 5] = -3.0            # 3 / 448 -> 2^-7 (0.0078125 >= 0.0066964)
+    x[1, 130] = 1e-6          # below the floor: 1e-4 / 448 -> 2^-22
+    x[2] = torch.linspace(-10, 10, 256)
+    q, e = act_quant_e8m0(x)
+    assert e.tolist()[0] == [127, 128] and e.tolist()[1] == [120, 105]
+    s = torch.exp2(e.float() - 127).repeat_interleave(128, 1)
+    back = q.view(torch.float8_e4m3fn).float() * s
+    assert back[0, 0].item() == 448.0 and back[1, 5].item() == -3.0
+    # e4m3 keeps 3 mantissa bits: every value within half a step of its input
+    rel = ((back - x).abs() / x.abs().clamp_min(1e-30))[x.abs() > 1e-3]
+    assert (rel <= 2 ** -4 + 1e-7).all()
+
+
+def test_fp8_block_matvec_matches_dense_product():
+    from hawking_b200.formats.safetensors import act_quant_e8m0, fp8_block_matvec
+    g = torch.Generator().manual_seed(3)
+    w = (torch.randn(256, 384, generator=g) * 2).to(torch.float8_e4m3fn)
+    we = torch.randint(120, 130, (2, 3), generator=g, dtype=torch.uint8)
+    x = torch.randn(384, generator=g)
+    aq, ae = act_quant_e8m0(x)
+    y = fp8_block_matvec(w.view(torch.uint8), we, aq, ae)
+    wd = w.float() * torch.exp2(we.float() - 127).repeat_interleave(128, 0).repeat_interleave(128, 1)
+    ad = aq.view(torch.float8_e4m3fn).float() * torch.exp2(ae.float() - 127).repeat_interleave(128)
+    assert torch.allclose(y.double(), wd.double() @ ad.double(), rtol=1e-5, atol=1e-5)
