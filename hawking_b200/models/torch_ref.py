@@ -45,8 +45,19 @@ def rmsnorm_ref(x: torch.Tensor, w: Optional[torch.Tensor], eps: float) -> torch
     return y * w.float() if w is not None else y
 
 
+# GGUF architectures of the reference's other families that this framework does not build: refused
+# at load with the reason instead of failing on a missing attention key
+NOT_BUILT_ARCHS = {
+    "rwkv6": "RWKV-6 (state-space decoder) is not built in this framework",
+    "rwkv7": "RWKV-7 (state-space decoder, WKV-7 recurrence) is not built in this framework",
+    "mamba": "Mamba (state-space decoder) is not built in this framework",
+}
+
+
 def config_from_gguf(m: GgufModel) -> ModelConfig:
     a = m.architecture
+    if a in NOT_BUILT_ARCHS:
+        raise ValueError(f"GGUF architecture {a!r}: {NOT_BUILT_ARCHS[a]}")
     if a == "deepseek2":
         from .deepseek_gguf import deepseek_config_from_gguf
         return deepseek_config_from_gguf(m)

@@ -47,3 +47,16 @@ def test_tensor_past_end_rejected(tmp_path, native):
     p.write_bytes(data[: len(data) - 64])
     with pytest.raises(RuntimeError, match="past end"):
         GgufModel(str(p))
+
+
+def test_state_space_architectures_are_refused_with_a_reason(tmp_path):
+    import numpy as np
+    import pytest as _pytest
+
+    from hawking_b200.formats.gguf import GgufBuilder, GgufModel
+    from hawking_b200.models.torch_ref import config_from_gguf
+    b = GgufBuilder("rwkv7")
+    b.add("token_embd.weight", np.zeros((8, 16), np.float32))
+    m = GgufModel(b.write(str(tmp_path / "r.gguf")))
+    with _pytest.raises(ValueError, match="rwkv7.*not built"):
+        config_from_gguf(m)
