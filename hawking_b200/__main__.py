@@ -4,7 +4,7 @@ Commands:
   serve      OpenAI-compatible HTTP server (see ``python -m hawking_b200 serve --help``)
   generate   one prompt through the engine, text out (``--gguf`` model or ``--preset`` random weights)
   tokenize   text -> token ids with a GGUF file's tokenizer (``--decode`` for ids -> text)
-  info       a GGUF / `.gravity` file's architecture, config and tensor summary
+  info       a GGUF / `.gravity` / `.safetensors` file's architecture, config and tensor summary
   verify     `.gravity` integrity: per-tensor and body sha256, gaps / overlaps (exit 1 on failure)
   bench      the headline decode / TTFT benchmark (bench.py) or one kernel microbenchmark
   doctor     environment report: Python, PyTorch, CUDA devices, the native and kernel modules, NCCL
@@ -91,8 +91,24 @@ def _cmd_info(a) -> int:
         out = {"format": ".gravity", "shards": len(g.shards),
                "tensors": sum(len(s.tensors) for s in g.shards.values()),
                "architecture": next(iter(g.shards.values())).architecture if g.shards else {}}
+    elif path.endswith(".safetensors"):
+        from .formats.safetensors import SafeTensors, SafetensorsError, native_scale_pairs
+        st = SafeTensors(path)
+        dtypes = {}
+        for t in st.tensors.values():
+            dtypes[t.dtype] = dtypes.get(t.dtype, 0) + 1
+        out = {"format": "safetensors", "tensors": len(st.tensors), "tensor_dtypes": dtypes,
+               "metadata": st.metadata}
+        try:
+            pairs = native_scale_pairs(st)
+            kinds = {}
+            for p in pairs.values():
+                kinds[p.kind] = kinds.get(p.kind, 0) + 1
+            out["native_pairs"] = kinds
+        except SafetensorsError as e:
+            out["native_pairs_error"] = str(e)
     else:
-        print(f"{path}: not a GGUF or .gravity file", file=sys.stderr)
+        print(f"{path}: not a GGUF, .gravity or .safetensors file", file=sys.stderr)
         return 2
     print(json.dumps(out, indent=1, default=str))
     return 0
@@ -193,7 +209,7 @@ def main(argv: Optional[List[str]] = None) -> int:
     t.add_argument("text")
     t.add_argument("--decode", action="store_true", help="the text is a list of ids to decode")
     t.add_argument("--no-special", action="store_true", help="do not add the BOS token")
-    i = sub.add_parser("info", help="summary of a GGUF or .gravity file")
+    i = sub.add_parser("info", help="summary of a GGUF, .gravity or .safetensors file")
     i.add_argument("path")
     v = sub.add_parser("verify", help="verify a .gravity shard or directory")
     v.add_argument("path")

@@ -41,3 +41,14 @@ def test_verify_gravity(tmp_path, capsys):
     data[-1] ^= 0xFF
     p.write_bytes(bytes(data))
     assert main(["verify", str(p)]) == 1
+
+
+def test_info_on_a_safetensors_checkpoint(tmp_path, capsys):
+    from hawking_b200.formats.safetensors import write_safetensors
+    p = write_safetensors(str(tmp_path / "m.safetensors"), {
+        "e.w1.weight": ("I8", (4, 16), bytes(64)), "e.w1.scale": ("F8_E8M0", (4, 1), bytes([127] * 4)),
+        "norm.weight": ("F32", (4,), np.ones(4, np.float32).tobytes())})
+    assert main(["info", p]) == 0
+    info = json.loads(capsys.readouterr().out)
+    assert info["format"] == "safetensors" and info["tensors"] == 3
+    assert info["native_pairs"] == {"fp4_e2m1_x2_e8m0": 1}
