@@ -16,7 +16,9 @@ Native pairs: a tensor ``<stem>.weight`` of dtype ``I8`` or ``F8_E4M3`` is paire
 A weight whose scale is missing, not rank-two E8M0 or not of the exact shape, a weight name that
 does not end in ``.weight``, and an E8M0 tensor that no weight claims are errors. The pairs load
 as mixed-table weights (kinds FP4 and FP8) with the exponents as exact fp32 scales (2^(e - 127)).
-``act_quant_e8m0`` and ``fp8_block_matvec`` state the source checkpoint's own fp8 linear (e4m3
+DeepSeek-V3 / R1 checkpoints pair an ``F8_E4M3`` ``<stem>.weight`` with an ``F32``
+``<stem>.weight_scale_inv`` [ceil(out / 128), K / 128] of per-block multipliers instead; those load
+as kind FP8 too. ``act_quant_e8m0`` and ``fp8_block_matvec`` state the source checkpoint's own fp8 linear (e4m3
 activations with a power-of-two scale per 128 columns) as a host reference.
 
 Parity: crates/hawking-core/src/gravity_deepseek_v4.rs:114-160 (NativeScalePairKind /
@@ -124,7 +126,7 @@ def write_safetensors(path: str, tensors: Mapping[str, Tuple[str, Tuple[int, ...
 
 @dataclass
 class NativePair:
-    kind: str            # "fp4_e2m1_x2_e8m0" or "fp8_e4m3_e8m0"
+    kind: str            # "fp4_e2m1_x2_e8m0", "fp8_e4m3_e8m0" or "fp8_e4m3_f32" (V3 weight_scale_inv)
     weight: str
     scale: str
     out_rows: int
@@ -140,6 +142,19 @@ def native_scale_pairs(st: SafeTensors) -> Dict[str, NativePair]:
     claimed = set()
     for name in st.names():
         w = st.tensors[name]
+        if w.dtype == "F8_E4M3" and name.endswith(".weight") and name + "_scale_inv" in st.tensors:
+            # DeepSeek-V3 / R1 convention: fp32 multipliers per 128 x 128 block (edge blocks partial)
+            s = st.tensors[name + "_scale_inv"]
+            if s.dtype != "F32" or len(w.shape) != 2 or len(s.shape) != 2:
+                raise SafetensorsError(f"{name}: weight_scale_inv must be a rank-two F32 tensor")
+            out_rows, k = w.shape
+            if k % FP8_BLOCK:
+                raise SafetensorsError(f"{name}: fp8 K {k} is not a multiple of {FP8_BLOCK}")
+            want = (-(-out_rows // FP8_BLOCK), k // FP8_BLOCK)
+            if tuple(s.shape) != want:
+                raise SafetensorsError(f"{name}: weight_scale_inv shape {list(s.shape)}, expected {list(want)}")
+            pairs[name] = NativePair("fp8_e4m3_f32", name, s.name, out_rows, k, k, *want)
+            continue
         if w.dtype == "I8":
             kind = "fp4_e2m1_x2_e8m0"
         elif w.dtype == "F8_E4M3":
@@ -190,8 +205,11 @@ def load_native_pair(st: SafeTensors, pair: NativePair, device):
     if pair.kind == "fp4_e2m1_x2_e8m0":
         e8 = torch.from_numpy(np.array(st.raw(pair.scale))).view(pair.scale_rows, pair.scale_cols)
         return MixedWeight.from_e2m1_e8m0(codes, e8, pair.out_rows, pair.logical_k, device)
-    sc = _e8m0_scales(st.raw(pair.scale)).view(pair.scale_rows, pair.scale_cols)
-    rows = sc.repeat_interleave(FP8_BLOCK, 0).contiguous()  # [out, K / 128]
+    if pair.kind == "fp8_e4m3_f32":
+        sc = torch.from_numpy(np.array(st.raw(pair.scale)).view(np.float32)).view(pair.scale_rows, pair.scale_cols)
+    else:
+        sc = _e8m0_scales(st.raw(pair.scale)).view(pair.scale_rows, pair.scale_cols)
+    rows = sc.repeat_interleave(FP8_BLOCK, 0)[: pair.out_rows].contiguous()  # [out, K / 128]
     return MixedWeight(FP8, 8, FP8_BLOCK, pair.out_rows, pair.logical_k, codes.to(device).contiguous(),
                        rows.to(device))
 

@@ -114,3 +114,23 @@ def test_fp8_block_matvec_matches_dense_product():
     wd = w.float() * torch.exp2(we.float() - 127).repeat_interleave(128, 0).repeat_interleave(128, 1)
     ad = aq.view(torch.float8_e4m3fn).float() * torch.exp2(ae.float() - 127).repeat_interleave(128)
     assert torch.allclose(y.double(), wd.double() @ ad.double(), rtol=1e-5, atol=1e-5)
+
+
+def test_deepseek_v3_weight_scale_inv_pairs(tmp_path):
+    g = torch.Generator().manual_seed(5)
+    w = (torch.randn(200, 256, generator=g) * 4).to(torch.float8_e4m3fn)   # 200 rows: a partial row block
+    inv = torch.rand(2, 2, generator=g) * 0.01 + 1e-3
+    st = _file(tmp_path, {
+        "model.layers.0.mlp.down_proj.weight": ("F8_E4M3", (200, 256), w.view(torch.uint8).numpy().tobytes()),
+        "model.layers.0.mlp.down_proj.weight_scale_inv": ("F32", (2, 2), inv.numpy().tobytes())})
+    pairs = native_scale_pairs(st)
+    p = pairs["model.layers.0.mlp.down_proj.weight"]
+    assert p.kind == "fp8_e4m3_f32" and (p.scale_rows, p.scale_cols) == (2, 2)
+    m = load_native_pair(st, p, "cpu")
+    assert m.kind == FP8 and (m.N, m.K) == (200, 256) and m.scales.shape == (200, 2)
+    blk = inv.repeat_interleave(128, 0)[:200].repeat_interleave(128, 1)
+    assert torch.equal(m.dequantize(), w.float() * blk)
+    bad = _file(tmp_path, {"a.weight": ("F8_E4M3", (200, 256), bytes(200 * 256)),
+                           "a.weight_scale_inv": ("F32", (1, 2), bytes(8))}, name="bad.safetensors")
+    with pytest.raises(SafetensorsError):
+        native_scale_pairs(bad)
