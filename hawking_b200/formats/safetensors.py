@@ -126,7 +126,7 @@ def write_safetensors(path: str, tensors: Mapping[str, Tuple[str, Tuple[int, ...
 
 @dataclass
 class NativePair:
-    kind: str            # "fp4_e2m1_x2_e8m0", "fp8_e4m3_e8m0" or "fp8_e4m3_f32" (V3 weight_scale_inv)
+    kind: str            # "native.fp4_e2m1fn_x2_e8m0", "native.fp8_e4m3fn_e8m0" or "native.fp8_e4m3fn_f32" (V3 weight_scale_inv)
     weight: str
     scale: str
     out_rows: int
@@ -153,12 +153,12 @@ def native_scale_pairs(st: SafeTensors) -> Dict[str, NativePair]:
             want = (-(-out_rows // FP8_BLOCK), k // FP8_BLOCK)
             if tuple(s.shape) != want:
                 raise SafetensorsError(f"{name}: weight_scale_inv shape {list(s.shape)}, expected {list(want)}")
-            pairs[name] = NativePair("fp8_e4m3_f32", name, s.name, out_rows, k, k, *want)
+            pairs[name] = NativePair("native.fp8_e4m3fn_f32", name, s.name, out_rows, k, k, *want)
             continue
         if w.dtype == "I8":
-            kind = "fp4_e2m1_x2_e8m0"
+            kind = "native.fp4_e2m1fn_x2_e8m0"
         elif w.dtype == "F8_E4M3":
-            kind = "fp8_e4m3_e8m0"
+            kind = "native.fp8_e4m3fn_e8m0"
         else:
             continue
         if not name.endswith(".weight"):
@@ -170,7 +170,7 @@ def native_scale_pairs(st: SafeTensors) -> Dict[str, NativePair]:
         if s.dtype != "F8_E8M0" or len(w.shape) != 2 or len(s.shape) != 2:
             raise SafetensorsError(f"{name}: the weight / scale pair is not rank-two with E8M0 scales")
         out_rows, packed_k = w.shape
-        if kind == "fp4_e2m1_x2_e8m0":
+        if kind == "native.fp4_e2m1fn_x2_e8m0":
             logical_k = 2 * packed_k
             if logical_k % FP4_BLOCK:
                 raise SafetensorsError(f"{name}: fp4 logical K {logical_k} is not a multiple of {FP4_BLOCK}")
@@ -202,10 +202,10 @@ def load_native_pair(st: SafeTensors, pair: NativePair, device):
     FP8 (codes kept, fp32 scale per 128 columns of each row, from the 128 x 128 blocks)."""
     from ..ops.mixed import FP8, MixedWeight
     codes = torch.from_numpy(np.array(st.raw(pair.weight))).view(pair.out_rows, pair.packed_k)
-    if pair.kind == "fp4_e2m1_x2_e8m0":
+    if pair.kind == "native.fp4_e2m1fn_x2_e8m0":
         e8 = torch.from_numpy(np.array(st.raw(pair.scale))).view(pair.scale_rows, pair.scale_cols)
         return MixedWeight.from_e2m1_e8m0(codes, e8, pair.out_rows, pair.logical_k, device)
-    if pair.kind == "fp8_e4m3_f32":
+    if pair.kind == "native.fp8_e4m3fn_f32":
         sc = torch.from_numpy(np.array(st.raw(pair.scale)).view(np.float32)).view(pair.scale_rows, pair.scale_cols)
     else:
         sc = _e8m0_scales(st.raw(pair.scale)).view(pair.scale_rows, pair.scale_cols)

@@ -51,4 +51,4 @@ def test_info_on_a_safetensors_checkpoint(tmp_path, capsys):
     assert main(["info", p]) == 0
     info = json.loads(capsys.readouterr().out)
     assert info["format"] == "safetensors" and info["tensors"] == 3
-    assert info["native_pairs"] == {"fp4_e2m1_x2_e8m0": 1}
+    assert info["native_pairs"] == {"native.fp4_e2m1fn_x2_e8m0": 1}

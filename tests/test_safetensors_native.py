@@ -125,7 +125,7 @@ def test_deepseek_v3_weight_scale_inv_pairs(tmp_path):
         "model.layers.0.mlp.down_proj.weight_scale_inv": ("F32", (2, 2), inv.numpy().tobytes())})
     pairs = native_scale_pairs(st)
     p = pairs["model.layers.0.mlp.down_proj.weight"]
-    assert p.kind == "fp8_e4m3_f32" and (p.scale_rows, p.scale_cols) == (2, 2)
+    assert p.kind == "native.fp8_e4m3fn_f32" and (p.scale_rows, p.scale_cols) == (2, 2)
     m = load_native_pair(st, p, "cpu")
     assert m.kind == FP8 and (m.N, m.K) == (200, 256) and m.scales.shape == (200, 2)
     blk = inv.repeat_interleave(128, 0)[:200].repeat_interleave(128, 1)
